@@ -1,0 +1,398 @@
+// k_rowops.cu -- row-wise ops of the op-chain: RMSNorm (+weight), adaLN modulate (with the
+// fused RMSNorm), per-head q/k RMSNorm + NeoX RoPE with strided / KV-cache destinations.
+//
+// All three are HBM-bound: one warp owns one row (or one head), the row is loaded once with
+// 16-byte vector loads into registers, reduced with warp shuffles, and written once. The
+// sum of squares is accumulated in double (the ggml-CPU rule), which makes the normalisation
+// scale identical to the CPU's; products and sums that ggml performs as separate graph nodes
+// are kept separately rounded (__fmul_rn / __fadd_rn) so no multiply-add is contracted.
+#include "common.cuh"
+
+namespace acb {
+
+// ---- vector store of N floats into an I/O type (N*size = 8, 16 or 32 bytes) ---------------
+template <int TO, int N> __device__ __forceinline__ void store_n(void * p, const float * f) {
+    using e = typename io<TO>::t;
+    constexpr int B = N * (int) sizeof(e);
+    static_assert(B == 8 || B == 16 || B == 32, "store width");
+    union {
+        uint4 u[B >= 16 ? B / 16 : 1];
+        uint2 h;
+        e     v[N];
+    } s;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+        s.v[i] = io<TO>::from_f(f[i]);
+    }
+    if constexpr (B == 8) {
+        *reinterpret_cast<uint2 *>(p) = s.h;
+    } else {
+#pragma unroll
+        for (int i = 0; i < B / 16; i++) {
+            reinterpret_cast<uint4 *>(p)[i] = s.u[i];
+        }
+    }
+}
+
+template <int N> __device__ __forceinline__ void load_w(const float * w, float * out) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+        float4 t   = __ldg(reinterpret_cast<const float4 *>(w + i));
+        out[i]     = t.x;
+        out[i + 1] = t.y;
+        out[i + 2] = t.z;
+        out[i + 3] = t.w;
+    }
+}
+
+// ---- RMSNorm / adaLN: one warp per row, row cached in registers ---------------------------
+// MODE 0: y = rms_norm(x)*w (w may be null)
+// MODE 1: y = (w ? rms_norm(x)*w : x) * (1 + scale) + shift
+template <int TI, int TO, int MAXV, int MODE>
+__global__ void __launch_bounds__(256) row_norm_kernel(const void * __restrict__ x, int64_t xs,
+                                                       const float * __restrict__ w, void * __restrict__ y,
+                                                       int64_t ys, int64_t rows, int cols, float eps,
+                                                       const float * __restrict__ scale,
+                                                       const float * __restrict__ shift, int64_t vec_stride,
+                                                       int64_t rows_per_sample) {
+    using VI              = vec16<TI>;
+    constexpr int N       = VI::N;
+    using ei              = typename io<TI>::t;
+    using eo              = typename io<TO>::t;
+    const int     lane    = threadIdx.x & 31;
+    const int64_t row     = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) {
+        return;
+    }
+    const char * xr   = reinterpret_cast<const char *>(x) + row * xs * (int64_t) sizeof(ei);
+    char *       yr   = reinterpret_cast<char *>(y) + row * ys * (int64_t) sizeof(eo);
+    const int    nvec = cols / N;
+
+    VI     v[MAXV];
+    double ss = 0.0;
+#pragma unroll
+    for (int i = 0; i < MAXV; i++) {
+        const int vi = lane + i * 32;
+        if (vi < nvec) {
+            v[i].load_stream(xr + (int64_t) vi * 16);
+        }
+    }
+    const bool do_norm = (MODE == 0) || (w != nullptr);
+    if (do_norm) {
+#pragma unroll
+        for (int i = 0; i < MAXV; i++) {
+            const int vi = lane + i * 32;
+            if (vi < nvec) {
+#pragma unroll
+                for (int j = 0; j < N; j++) {
+                    float f = v[i].get(j);
+                    ss += (double) __fmul_rn(f, f);
+                }
+            }
+        }
+        ss = warp_sum(ss);
+    }
+    const float sc = do_norm ? rms_scale(ss, cols, eps) : 1.0f;
+    const float * scl = nullptr;
+    const float * shf = nullptr;
+    if (MODE == 1) {
+        const int64_t s = row / rows_per_sample;
+        scl             = scale + s * vec_stride;
+        shf             = shift + s * vec_stride;
+    }
+#pragma unroll
+    for (int i = 0; i < MAXV; i++) {
+        const int vi = lane + i * 32;
+        if (vi < nvec) {
+            float o[N];
+            float wv[N];
+            if (w) {
+                load_w<N>(w + (int64_t) vi * N, wv);
+            }
+#pragma unroll
+            for (int j = 0; j < N; j++) {
+                float f = v[i].get(j);
+                if (do_norm) {
+                    f = __fmul_rn(f, sc);
+                    if (w) {
+                        f = __fmul_rn(f, wv[j]);
+                    }
+                }
+                o[j] = f;
+            }
+            if (MODE == 1) {
+                float a[N], b[N];
+                load_w<N>(scl + (int64_t) vi * N, a);
+                load_w<N>(shf + (int64_t) vi * N, b);
+#pragma unroll
+                for (int j = 0; j < N; j++) {
+                    o[j] = __fadd_rn(__fmul_rn(o[j], __fadd_rn(a[j], 1.0f)), b[j]);
+                }
+            }
+            store_n<TO, N>(yr + (int64_t) vi * N * (int64_t) sizeof(eo), o);
+        }
+    }
+}
+
+// Fallback for unaligned / odd-width rows: scalar loads, two passes over the row.
+template <int TI, int TO, int MODE>
+__global__ void __launch_bounds__(256) row_norm_scalar_kernel(const void * __restrict__ x, int64_t xs,
+                                                              const float * __restrict__ w, void * __restrict__ y,
+                                                              int64_t ys, int64_t rows, int cols, float eps,
+                                                              const float * __restrict__ scale,
+                                                              const float * __restrict__ shift, int64_t vec_stride,
+                                                              int64_t rows_per_sample) {
+    using ei           = typename io<TI>::t;
+    using eo           = typename io<TO>::t;
+    const int     lane = threadIdx.x & 31;
+    const int64_t row  = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= rows) {
+        return;
+    }
+    const ei * xr      = reinterpret_cast<const ei *>(x) + row * xs;
+    eo *       yr      = reinterpret_cast<eo *>(y) + row * ys;
+    const bool do_norm = (MODE == 0) || (w != nullptr);
+    double     ss      = 0.0;
+    if (do_norm) {
+        for (int i = lane; i < cols; i += 32) {
+            float f = io<TI>::to_f(xr[i]);
+            ss += (double) __fmul_rn(f, f);
+        }
+        ss = warp_sum(ss);
+    }
+    const float   sc = do_norm ? rms_scale(ss, cols, eps) : 1.0f;
+    const int64_t s  = MODE == 1 ? row / rows_per_sample : 0;
+    for (int i = lane; i < cols; i += 32) {
+        float f = io<TI>::to_f(xr[i]);
+        if (do_norm) {
+            f = __fmul_rn(f, sc);
+            if (w) {
+                f = __fmul_rn(f, w[i]);
+            }
+        }
+        if (MODE == 1) {
+            f = __fadd_rn(__fmul_rn(f, __fadd_rn(scale[s * vec_stride + i], 1.0f)), shift[s * vec_stride + i]);
+        }
+        yr[i] = io<TO>::from_f(f);
+    }
+}
+
+template <int TI, int TO, int MODE>
+static acb_status launch_row_norm(const void * x, int64_t xs, const float * w, void * y, int64_t ys, int64_t rows,
+                                  int cols, float eps, const float * scale, const float * shift, int64_t vs,
+                                  int64_t rps, cudaStream_t st) {
+    constexpr int NI    = vec16<TI>::N;
+    const int     warps = 8;
+    const dim3    grid((unsigned) ((rows + warps - 1) / warps));
+    const int     si = (int) sizeof(typename io<TI>::t), so = (int) sizeof(typename io<TO>::t);
+    const bool    aligned = cols % NI == 0 && (reinterpret_cast<uintptr_t>(x) % 16) == 0 &&
+                         (reinterpret_cast<uintptr_t>(y) % 16) == 0 && (xs * si) % 16 == 0 && (ys * so) % 16 == 0 &&
+                         (w == nullptr || reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                         (MODE == 0 || ((reinterpret_cast<uintptr_t>(scale) % 16) == 0 &&
+                                        (reinterpret_cast<uintptr_t>(shift) % 16) == 0 && vs % 4 == 0)) &&
+                         (NI * so) >= 8;
+    const int nvec = cols / NI;
+    if (aligned && nvec <= 32 * 24) {
+        if (nvec <= 32 * 4) {
+            row_norm_kernel<TI, TO, 4, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
+                                                                         shift, vs, rps);
+        } else if (nvec <= 32 * 8) {
+            row_norm_kernel<TI, TO, 8, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
+                                                                         shift, vs, rps);
+        } else if (nvec <= 32 * 16) {
+            row_norm_kernel<TI, TO, 16, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
+                                                                          shift, vs, rps);
+        } else {
+            row_norm_kernel<TI, TO, 24, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
+                                                                          shift, vs, rps);
+        }
+    } else {
+        row_norm_scalar_kernel<TI, TO, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
+                                                                          shift, vs, rps);
+    }
+    return launch_status();
+}
+
+template <int MODE>
+static acb_status dispatch_row_norm(int ti, int to, const void * x, int64_t xs, const float * w, void * y,
+                                    int64_t ys, int64_t rows, int cols, float eps, const float * scale,
+                                    const float * shift, int64_t vs, int64_t rps, cudaStream_t st) {
+#define ACB_RN(A, B)                                                                                          \
+    if (ti == A && to == B) {                                                                                 \
+        return launch_row_norm<A, B, MODE>(x, xs, w, y, ys, rows, cols, eps, scale, shift, vs, rps, st);      \
+    }
+    ACB_RN(ACB_TYPE_F32, ACB_TYPE_F32)
+    ACB_RN(ACB_TYPE_F32, ACB_TYPE_BF16)
+    ACB_RN(ACB_TYPE_F32, ACB_TYPE_F16)
+    ACB_RN(ACB_TYPE_BF16, ACB_TYPE_BF16)
+    ACB_RN(ACB_TYPE_BF16, ACB_TYPE_F32)
+    ACB_RN(ACB_TYPE_F16, ACB_TYPE_F16)
+    ACB_RN(ACB_TYPE_F16, ACB_TYPE_F32)
+#undef ACB_RN
+    return ACB_ERR_UNSUPPORTED;
+}
+
+// ---- per-head q/k RMSNorm + NeoX RoPE ------------------------------------------------------
+// One warp per (token, head). Lane l owns E = D/64 consecutive elements of the first half
+// starting at l*E and the matching elements of the second half, so each NeoX pair (i, i+D/2)
+// lives in one lane.
+template <int TI, int TO, int E>
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(
+    const void * __restrict__ src, int64_t sts, void * __restrict__ dst, int64_t dts, int64_t dhs, int64_t dps,
+    int64_t n_tok, int n_heads, const float * __restrict__ w, float eps, const int32_t * __restrict__ pos,
+    const float * __restrict__ rope, int max_pos, int * __restrict__ err) {
+    using ei              = typename io<TI>::t;
+    using eo              = typename io<TO>::t;
+    constexpr int D       = 64 * E;
+    constexpr int HALF    = D / 2;
+    const int     lane    = threadIdx.x & 31;
+    const int64_t item    = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= n_tok * n_heads) {
+        return;
+    }
+    const int64_t t = item / n_heads;
+    const int     h = (int) (item - t * n_heads);
+    int           p = 0;
+    if (pos) {
+        p = __ldg(pos + t);
+        if (p < 0 || p >= max_pos) {
+            if (lane == 0 && err) {
+                atomicOr(err, ACB_DEVERR_POS_RANGE);
+            }
+            return;
+        }
+    }
+    const ei * s = reinterpret_cast<const ei *>(src) + t * sts + (int64_t) h * D + lane * E;
+    float      a[E], b[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        a[e] = io<TI>::to_f(s[e]);
+        b[e] = io<TI>::to_f(s[HALF + e]);
+    }
+    if (w) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            ss += (double) __fmul_rn(a[e], a[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            ss += (double) __fmul_rn(b[e], b[e]);
+        }
+        ss             = warp_sum(ss);
+        const float sc = rms_scale(ss, D, eps);
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * E + e));
+            b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(w + HALF + lane * E + e));
+        }
+    }
+    eo * d = reinterpret_cast<eo *>(dst) + t * dts + (int64_t) h * dhs + (int64_t) p * dps + lane * E;
+    if (rope) {
+        const float * c = rope + (int64_t) p * D + 2 * lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            const float cs = __ldg(c + 2 * e), sn = __ldg(c + 2 * e + 1);
+            const float x0 = a[e], x1 = b[e];
+            a[e]           = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            b[e]           = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        d[e]        = io<TO>::from_f(a[e]);
+        d[HALF + e] = io<TO>::from_f(b[e]);
+    }
+}
+
+template <int TI, int TO>
+static acb_status launch_qk(const void * src, int64_t sts, void * dst, int64_t dts, int64_t dhs, int64_t dps,
+                            int64_t n_tok, int n_heads, int D, const float * w, float eps, const int32_t * pos,
+                            const float * rope, int max_pos, int * err, cudaStream_t st) {
+    const int64_t items = n_tok * n_heads;
+    const int     warps = 8;
+    const dim3    grid((unsigned) ((items + warps - 1) / warps));
+    switch (D) {
+        case 64:
+            qk_norm_rope_kernel<TI, TO, 1><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads,
+                                                                       w, eps, pos, rope, max_pos, err);
+            break;
+        case 128:
+            qk_norm_rope_kernel<TI, TO, 2><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads,
+                                                                       w, eps, pos, rope, max_pos, err);
+            break;
+        case 256:
+            qk_norm_rope_kernel<TI, TO, 4><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads,
+                                                                       w, eps, pos, rope, max_pos, err);
+            break;
+        default:
+            return ACB_ERR_UNSUPPORTED;
+    }
+    return launch_status();
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" acb_status acb_rms_norm(const void * x, int x_type, int64_t x_stride, const float * w, void * y,
+                                   int y_type, int64_t y_stride, int64_t rows, int cols, float eps,
+                                   acb_stream_t stream) {
+    if (!x || !y || rows < 0 || cols <= 0 || x_stride < cols || y_stride < cols) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (rows == 0) {
+        return ACB_OK;
+    }
+    return dispatch_row_norm<0>(x_type, y_type, x, x_stride, w, y, y_stride, rows, cols, eps, nullptr, nullptr, 0, 1,
+                                (cudaStream_t) stream);
+}
+
+extern "C" acb_status acb_adaln_modulate(const void * x, int x_type, const float * norm_w, float eps,
+                                         const float * scale, const float * shift, int64_t vec_stride, void * y,
+                                         int y_type, int64_t samples, int64_t rows_per_sample, int H,
+                                         acb_stream_t stream) {
+    if (!x || !y || !scale || !shift || samples < 0 || rows_per_sample < 0 || H <= 0 || vec_stride < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (samples * rows_per_sample == 0) {
+        return ACB_OK;
+    }
+    return dispatch_row_norm<1>(x_type, y_type, x, H, norm_w, y, H, samples * rows_per_sample, H, eps, scale, shift,
+                                vec_stride, rows_per_sample, (cudaStream_t) stream);
+}
+
+extern "C" acb_status acb_qk_norm_rope(const void * src, int src_type, int64_t src_tok_stride, void * dst,
+                                       int dst_type, int64_t dst_tok_stride, int64_t dst_head_stride,
+                                       int64_t dst_pos_stride, int64_t n_tok, int n_heads, int head_dim,
+                                       const float * norm_w, float eps, const int32_t * pos,
+                                       const float * rope_table, int max_pos, int * err_flag,
+                                       acb_stream_t stream) {
+    if (!src || !dst || n_tok < 0 || n_heads <= 0 || head_dim <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if ((rope_table || dst_pos_stride != 0) && (!pos || max_pos <= 0)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (head_dim % 64 != 0 || head_dim > 256) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (n_tok == 0) {
+        return ACB_OK;
+    }
+    cudaStream_t st = (cudaStream_t) stream;
+#define ACB_QK(A, B)                                                                                             \
+    if (src_type == A && dst_type == B) {                                                                        \
+        return launch_qk<A, B>(src, src_tok_stride, dst, dst_tok_stride, dst_head_stride, dst_pos_stride, n_tok, \
+                               n_heads, head_dim, norm_w, eps, pos, rope_table, max_pos, err_flag, st);          \
+    }
+    ACB_QK(ACB_TYPE_F32, ACB_TYPE_F32)
+    ACB_QK(ACB_TYPE_F32, ACB_TYPE_F16)
+    ACB_QK(ACB_TYPE_F32, ACB_TYPE_BF16)
+    ACB_QK(ACB_TYPE_BF16, ACB_TYPE_BF16)
+    ACB_QK(ACB_TYPE_BF16, ACB_TYPE_F32)
+    ACB_QK(ACB_TYPE_BF16, ACB_TYPE_F16)
+    ACB_QK(ACB_TYPE_F16, ACB_TYPE_F16)
+#undef ACB_QK
+    return ACB_ERR_UNSUPPORTED;
+}

@@ -1,0 +1,136 @@
+/*
+ * acb.h -- C ABI of libacb, the B200 (sm_100a) implementation of acestep.cpp's per-layer
+ * transformer op-chain.
+ *
+ * Conventions
+ *   - Every entry point returns an acb_status (0 = ACB_OK) and never exits the process.
+ *   - Tensor arguments are device pointers with explicit element strides; nothing here takes
+ *     a framework tensor type. Host arguments are marked "host".
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream). All kernels are enqueued
+ *     asynchronously; a launch failure is reported as ACB_ERR_CUDA.
+ *   - Type ids are the GGUF/ggml tensor type ids (acb_type), so GGUF blocks are consumed
+ *     byte-for-byte with no repacking.
+ *   - Layouts use ggml order translated to row-major: a ggml activation [H, S] is rows[S][H];
+ *     a ggml weight [K, N] is N rows of K elements with quant blocks running along K.
+ *   - `err_flag` (optional device int) receives a bitwise OR of ACB_DEVERR_* bits when a
+ *     kernel meets an out-of-range index; the offending row is written as zeros and nothing is
+ *     read out of bounds.
+ *
+ * Each function names the reference interface (file:line in acestep.cpp) whose ggml graph node
+ * it replaces.
+ */
+#ifndef ACB_H
+#define ACB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#    define ACB_API __attribute__((visibility("default")))
+#else
+#    define ACB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st * acb_stream_t; /* == cudaStream_t */
+
+typedef enum {
+    ACB_OK               = 0,
+    ACB_ERR_INVALID_ARG  = 1, /* null pointer, bad size, bad stride */
+    ACB_ERR_UNSUPPORTED  = 2, /* type / shape combination not implemented */
+    ACB_ERR_CUDA         = 3, /* a CUDA runtime call or kernel launch failed */
+    ACB_ERR_OUT_OF_RANGE = 4, /* id, position or kv length beyond its table */
+    ACB_ERR_OOM          = 5, /* device or host allocation failed */
+    ACB_ERR_IO           = 6, /* file open / map / read failed */
+    ACB_ERR_FORMAT       = 7, /* malformed or truncated GGUF, missing tensor */
+    ACB_ERR_DEVICE       = 8, /* a kernel reported an error through its device flag */
+} acb_status;
+
+typedef enum {
+    ACB_TYPE_F32  = 0,
+    ACB_TYPE_F16  = 1,
+    ACB_TYPE_Q8_0 = 8,
+    ACB_TYPE_Q4_K = 12,
+    ACB_TYPE_Q6_K = 14,
+    ACB_TYPE_Q8_K = 15,
+    ACB_TYPE_I32  = 26,
+    ACB_TYPE_BF16 = 30,
+} acb_type;
+
+enum {
+    ACB_DEVERR_ID_RANGE  = 1, /* get_rows id outside [0, n_rows) */
+    ACB_DEVERR_POS_RANGE = 2, /* rope / kv position outside [0, max_pos) */
+    ACB_DEVERR_TIMEOUT   = 4, /* a bounded device-side wait gave up */
+};
+
+/* ---- library ------------------------------------------------------------------------------ */
+
+ACB_API int          acb_version(void);                  /* (major << 16) | (minor << 8) | patch */
+ACB_API const char * acb_status_string(int status);      /* static string */
+ACB_API int          acb_last_cuda_error(void);          /* cudaError_t of the last ACB_ERR_CUDA */
+ACB_API int64_t      acb_row_bytes(int type, int64_t n); /* bytes of a row of n elements, -1 if invalid */
+
+/* RoPE table for mode NEOX (freq_scale 1, ext_factor 0, attn_factor 1), host memory:
+ * table[p][2i] = cos(theta_i(p)), table[p][2i+1] = sin(theta_i(p)), i < head_dim/2, where
+ * theta_0 = p and theta_{i+1} = theta_i * base^(-2/head_dim) in float (the ggml rope cache).
+ * Replaces the angle computation inside ggml_rope_ext(..., mode 2, ...) at
+ * src/qwen3-enc.h:172-173, src/qwen3-lm.h:378-379,666-667, src/dit-graph.h:195-197. */
+ACB_API acb_status acb_rope_table_host(float * table, int max_pos, int head_dim, float base);
+
+/* ---- row ops (config 2a-2d of the op-chain) ------------------------------------------------ */
+
+/* y[r] = rms_norm(x[r], eps) * w (w NULL: plain rms_norm). x/y types F32, BF16 or F16.
+ * Replaces ggml_rms_norm + ggml_mul: qwen3_rms_norm (src/qwen3-enc.h:114-120),
+ * dit_ggml_rms_norm_weighted (src/dit-graph.h:24-30). */
+ACB_API acb_status acb_rms_norm(const void * x, int x_type, int64_t x_stride, const float * w, void * y, int y_type,
+                        int64_t y_stride, int64_t rows, int cols, float eps, acb_stream_t stream);
+
+/* Per-head RMSNorm * norm_w followed by NeoX RoPE, gathered from and scattered to strided
+ * layouts (also the f16 KV-cache write). Source element (t, h, d) is
+ * src[t*src_tok_stride + h*head_dim + d]; destination element is
+ * dst[t*dst_tok_stride + h*dst_head_stride + pos[t]*dst_pos_stride + d].
+ * norm_w NULL skips the norm; rope_table NULL skips the rotation (pos may then be NULL when
+ * dst_pos_stride is 0). rope_table is [max_pos][head_dim] from acb_rope_table_host, on device.
+ * head_dim must be a multiple of 64 and at most 256. dst_type F32, F16 or BF16.
+ * Replaces the q/k-norm + ggml_rope_ext + ggml_cpy(->f16 cache) chain of
+ * qwen3_build_self_attn (src/qwen3-enc.h:159-174), qw3lm_build_attn (src/qwen3-lm.h:366-406),
+ * qw3lm_forward_batch (src/qwen3-lm.h:654-703) and dit_ggml_build_self_attn
+ * (src/dit-graph.h:175-198). */
+ACB_API acb_status acb_qk_norm_rope(const void * src, int src_type, int64_t src_tok_stride, void * dst, int dst_type,
+                            int64_t dst_tok_stride, int64_t dst_head_stride, int64_t dst_pos_stride, int64_t n_tok,
+                            int n_heads, int head_dim, const float * norm_w, float eps, const int32_t * pos,
+                            const float * rope_table, int max_pos, int * err_flag, acb_stream_t stream);
+
+/* out[r][i] = silu(g[r][i]) * u[r][i], silu(v) = v / (1 + exp(-v)). g = gu + r*gu_stride,
+ * u = g + up_offset (fused [gate(F) | up(F)] rows: up_offset = F, gu_stride = 2F).
+ * Replaces ggml_swiglu / ggml_swiglu_split (src/qwen3-enc.h:217,221; src/dit-graph.h:259,264). */
+ACB_API acb_status acb_swiglu(const void * gu, int gu_type, int64_t gu_stride, int64_t up_offset, void * out, int out_type,
+                      int64_t out_stride, int64_t rows, int64_t F, acb_stream_t stream);
+
+/* y = n * (1 + scale[s]) + shift[s] with n = rms_norm(x)*norm_w (norm_w NULL: n = x).
+ * x/y [samples][rows_per_sample][H]; scale/shift F32 device vectors, vec_stride 0 = one vector
+ * for every sample, H = one per sample. Replaces dit_ggml_rms_norm_weighted + dit_ggml_adaln
+ * (src/dit-graph.h:24-30, 54-64, 405-406, 438-439, 603-604). */
+ACB_API acb_status acb_adaln_modulate(const void * x, int x_type, const float * norm_w, float eps, const float * scale,
+                              const float * shift, int64_t vec_stride, void * y, int y_type, int64_t samples,
+                              int64_t rows_per_sample, int H, acb_stream_t stream);
+
+/* out = r + o * gate[s] (gate raw, no sigmoid); layouts as acb_adaln_modulate; out may alias r.
+ * Replaces dit_ggml_gated_add (src/dit-graph.h:70-76, 420, 445). */
+ACB_API acb_status acb_gated_residual(const void * r, const void * o, int io_type, const float * gate, int64_t vec_stride,
+                              void * out, int64_t samples, int64_t rows_per_sample, int H, acb_stream_t stream);
+
+/* out[i][:] = dequant(table[ids[i]][:]) for table rows of `cols` elements in table_type
+ * (F32, F16, BF16, Q8_0, Q4_K, Q6_K); out_type F32, BF16 or F16. Bit-exact with the ggml
+ * dequantizers. Replaces ggml_get_rows (src/qwen3-enc.h:390,465; src/qwen3-lm.h:464,626). */
+ACB_API acb_status acb_get_rows(const void * table, int table_type, int64_t n_rows, int64_t cols, const int32_t * ids,
+                        int64_t n_ids, void * out, int out_type, int64_t out_stride, int * err_flag,
+                        acb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

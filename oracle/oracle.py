@@ -1,0 +1,398 @@
+"""numpy front end of the C oracle (oracle/_build/libacb_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and bench.py's
+CPU-baseline leg, never by the product library. The C sources restate the ggml-CPU arithmetic
+of the reference's op-chain (src/qwen3-enc.h, src/qwen3-lm.h, src/dit-graph.h); see
+acb_oracle.h for the float rules.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libacb_oracle.so")
+
+F32, F16, Q8_0, Q4_K, Q6_K, Q8_K, BF16 = 0, 1, 8, 12, 14, 15, 30
+BLOCK = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q8_K: (256, 292)}
+
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        P, I64, I, F = C.c_void_p, C.c_int64, C.c_int, C.c_float
+        sig = {
+            "orc_f16_to_f32": (C.c_float, [C.c_uint16]),
+            "orc_f32_to_f16": (C.c_uint16, [F]),
+            "orc_f32_to_bf16": (C.c_uint16, [F]),
+            "orc_row_bytes": (I64, [I, I64]),
+            "orc_dequant_row": (I, [I, P, P, I64]),
+            "orc_quantize_row_q8_0": (None, [P, P, I64]),
+            "orc_quantize_row_q8_K": (None, [P, P, I64]),
+            "orc_quantize_row_q4_K": (None, [P, P, I64]),
+            "orc_quantize_row_q6_K": (None, [P, P, I64]),
+            "orc_get_rows": (I, [I, P, I64, I64, P, I64, P]),
+            "orc_rms_norm": (None, [P, P, P, I64, I64, F]),
+            "orc_rope_cache": (None, [P, P, I64, I, F]),
+            "orc_qk_norm_rope": (None, [P, I64, P, I64, I64, I, I, P, F, P]),
+            "orc_swiglu": (None, [P, I64, P, I64, P, I64, I64]),
+            "orc_adaln": (None, [P, P, F, P, P, I64, P, I64, I64, I64]),
+            "orc_gated_residual": (None, [P, P, P, I64, P, I64, I64, I64]),
+            "orc_mul_mat": (I, [I, P, I64, I64, P, I64, P]),
+            "orc_attention": (None, [P, I64, P, P, I, I64, I64, P, P, I64, I64, I64, I, I, I, F]),
+            "orc_timestep_embedding": (None, [F, I, I, P]),
+            "orc_set_threads": (None, [I]),
+            "orc_get_threads": (I, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def row_bytes(qtype: int, n: int) -> int:
+    be, bb = BLOCK[qtype]
+    assert n % be == 0
+    return n // be * bb
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+def get_threads() -> int:
+    return lib().orc_get_threads()
+
+
+# ---- formats -------------------------------------------------------------------------------
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even bf16 bits of float32 values (ggml_compute_fp32_to_bf16)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + (0x7FFF + ((u >> 16) & 1))) >> 16).astype(np.uint16)
+    return np.where(nan, ((u >> 16) | 64).astype(np.uint16), r)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+def quantize(x: np.ndarray, qtype: int) -> np.ndarray:
+    """Rows of x [..., K] -> raw block bytes [..., row_bytes] (Q8_0, Q8_K, Q4_K, Q6_K, F32, F16, BF16)."""
+    x = _f32(x)
+    K = x.shape[-1]
+    rows = x.reshape(-1, K)
+    if qtype == F32:
+        return rows.view(np.uint8).reshape(*x.shape[:-1], K * 4)
+    if qtype == F16:
+        return rows.astype(np.float16).view(np.uint8).reshape(*x.shape[:-1], K * 2)
+    if qtype == BF16:
+        return f32_to_bf16_bits(rows).view(np.uint8).reshape(*x.shape[:-1], K * 2)
+    rb = row_bytes(qtype, K)
+    out = np.empty((rows.shape[0], rb), dtype=np.uint8)
+    fn = {Q8_0: lib().orc_quantize_row_q8_0, Q8_K: lib().orc_quantize_row_q8_K,
+          Q4_K: lib().orc_quantize_row_q4_K, Q6_K: lib().orc_quantize_row_q6_K}[qtype]
+    fn(_p(rows), _p(out), rows.size)
+    return out.reshape(*x.shape[:-1], rb)
+
+
+def dequantize(raw: np.ndarray, qtype: int, K: int) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    rb = row_bytes(qtype, K)
+    rows = raw.reshape(-1, rb)
+    out = np.empty((rows.shape[0], K), dtype=np.float32)
+    rc = lib().orc_dequant_row(qtype, _p(rows), _p(out), rows.shape[0] * K)
+    assert rc == 0
+    return out.reshape(*raw.shape[:-1], K)
+
+
+# ---- ops -----------------------------------------------------------------------------------
+
+def get_rows(qtype: int, table: np.ndarray, cols: int, ids: np.ndarray) -> tuple[int, np.ndarray]:
+    table = np.ascontiguousarray(table, dtype=np.uint8)
+    n_rows = table.size // row_bytes(qtype, cols)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    out = np.zeros((ids.size, cols), dtype=np.float32)
+    rc = lib().orc_get_rows(qtype, _p(table), n_rows, cols, _p(ids), ids.size, _p(out))
+    return rc, out
+
+
+def rms_norm(x, w, eps):
+    x = _f32(x)
+    cols = x.shape[-1]
+    y = np.empty_like(x)
+    lib().orc_rms_norm(_p(x), _p(None if w is None else _f32(w)), _p(y), x.size // cols, cols, eps)
+    return y
+
+
+def rope_cache(pos, head_dim, base):
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    c = np.empty((pos.size, head_dim), dtype=np.float32)
+    lib().orc_rope_cache(_p(c), _p(pos), pos.size, head_dim, base)
+    return c
+
+
+def qk_norm_rope(x, w, eps, rope):
+    """x [T, Hh, D] -> per-head rms_norm*w then NeoX rope with table rows rope[T, D]."""
+    x = _f32(x)
+    T, Hh, D = x.shape
+    y = np.empty_like(x)
+    rope = None if rope is None else _f32(rope)
+    lib().orc_qk_norm_rope(_p(x), Hh * D, _p(y), Hh * D, T, Hh, D, _p(None if w is None else _f32(w)), eps,
+                           _p(rope))
+    return y
+
+
+def swiglu(g, u):
+    g, u = _f32(g), _f32(u)
+    F = g.shape[-1]
+    rows = g.size // F
+    out = np.empty_like(g)
+    lib().orc_swiglu(_p(g), F, _p(u), F, _p(out), rows, F)
+    return out
+
+
+def adaln(x, w, eps, scale, shift):
+    """x [S, T, H]; scale/shift [H] (shared) or [S, H] (per sample)."""
+    x = _f32(x)
+    S, T, H = x.shape
+    scale, shift = _f32(scale), _f32(shift)
+    vs = 0 if scale.ndim == 1 else H
+    y = np.empty_like(x)
+    lib().orc_adaln(_p(x), _p(None if w is None else _f32(w)), eps, _p(scale), _p(shift), vs, _p(y), S, T, H)
+    return y
+
+
+def gated_residual(r, o, gate):
+    r, o, gate = _f32(r), _f32(o), _f32(gate)
+    S, T, H = r.shape
+    vs = 0 if gate.ndim == 1 else H
+    out = np.empty_like(r)
+    lib().orc_gated_residual(_p(r), _p(o), _p(gate), vs, _p(out), S, T, H)
+    return out
+
+
+def mul_mat(wtype, W_raw, N, K, x):
+    x = _f32(x)
+    M = x.size // K
+    y = np.empty((M, N), dtype=np.float32)
+    rc = lib().orc_mul_mat(wtype, _p(np.ascontiguousarray(W_raw)), N, K, _p(x), M, _p(y))
+    assert rc == 0
+    return y.reshape(*x.shape[:-1], N)
+
+
+def attention(q, k, v, kv_type, mask, scale, kv_head_major=False):
+    """q [Sq, Hq, D] f32; k/v [Skv, Hkv, D] (kv_type F32 float32 or F16 uint16 bits), or
+    [Hkv, Skv, D] when kv_head_major. mask [Sq, Skv] additive or None. Returns [Sq, Hq, D]."""
+    q = _f32(q)
+    Sq, Hq, D = q.shape
+    if kv_head_major:
+        Hkv, Skv, _ = k.shape
+        tok_stride, head_stride = D, Skv * D
+    else:
+        Skv, Hkv, _ = k.shape
+        tok_stride, head_stride = Hkv * D, D
+    dt = np.uint16 if kv_type == F16 else np.float32
+    k = np.ascontiguousarray(k, dtype=dt)
+    v = np.ascontiguousarray(v, dtype=dt)
+    out = np.empty_like(q)
+    m = None if mask is None else _f32(mask)
+    lib().orc_attention(_p(q), Hq * D, _p(k), _p(v), kv_type, tok_stride, head_stride, _p(m), _p(out), Hq * D,
+                        Sq, Skv, Hq, Hkv, D, scale)
+    return out
+
+
+def timestep_embedding(t, dim=256, max_period=10000):
+    out = np.empty(dim, dtype=np.float32)
+    lib().orc_timestep_embedding(t, dim, max_period, _p(out))
+    return out
+
+
+# ---- model forwards (acb_oracle_models.h) ----------------------------------------------------
+
+class Tensor(C.Structure):
+    _fields_ = [("type", C.c_int), ("data", C.c_void_p), ("K", C.c_int64), ("N", C.c_int64)]
+
+
+class Qwen3Layer(C.Structure):
+    _fields_ = [(n, Tensor) for n in ("attn_norm", "qkv", "q_norm", "k_norm", "o", "post_norm", "gate_up", "down")]
+
+
+class Qwen3(C.Structure):
+    _fields_ = [("n_layers", C.c_int), ("H", C.c_int), ("F", C.c_int), ("Nh", C.c_int), ("Nkv", C.c_int),
+                ("D", C.c_int), ("V", C.c_int), ("rope_theta", C.c_float), ("eps", C.c_float),
+                ("embed", Tensor), ("final_norm", Tensor), ("layers", C.POINTER(Qwen3Layer))]
+
+
+class KV(C.Structure):
+    _fields_ = [("k", C.c_void_p), ("v", C.c_void_p), ("n_sets", C.c_int), ("max_seq", C.c_int)]
+
+
+class DiTTemb(C.Structure):
+    _fields_ = [(n, Tensor) for n in ("l1_w", "l1_b", "l2_w", "l2_b", "tp_w", "tp_b")]
+
+
+class DiTLayer(C.Structure):
+    _fields_ = [(n, Tensor) for n in ("sa_norm", "sa_qkv", "sa_q_norm", "sa_k_norm", "sa_o", "ca_norm", "ca_qkv",
+                                      "ca_q_norm", "ca_k_norm", "ca_o", "mlp_norm", "gate_up", "down",
+                                      "scale_shift")] + [("layer_type", C.c_int)]
+
+
+class DiT(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "H", "F", "Nh", "Nkv", "D", "in_ch", "out_ch", "P",
+                                       "sliding_window", "H_enc")] + \
+               [("rope_theta", C.c_float), ("eps", C.c_float), ("te", DiTTemb), ("te_r", DiTTemb),
+                ("proj_in_w", Tensor), ("proj_in_b", Tensor), ("cond_w", Tensor), ("cond_b", Tensor),
+                ("layers", C.POINTER(DiTLayer)), ("norm_out", Tensor), ("out_ss", Tensor),
+                ("proj_out_w", Tensor), ("proj_out_b", Tensor)]
+
+
+def _models_lib():
+    L = lib()
+    if not getattr(L, "_models_bound", False):
+        P, I, F = C.c_void_p, C.c_int, C.c_float
+        L.orc_qwen3_encode.restype = I
+        L.orc_qwen3_encode.argtypes = [C.POINTER(Qwen3), P, I, P]
+        L.orc_qw3lm_prefill.restype = I
+        L.orc_qw3lm_prefill.argtypes = [C.POINTER(Qwen3), C.POINTER(KV), I, I, P, I, P, I, I, P]
+        L.orc_qw3lm_decode.restype = I
+        L.orc_qw3lm_decode.argtypes = [C.POINTER(Qwen3), C.POINTER(KV), I, P, P, I, P, I, I]
+        L.orc_dit_forward.restype = I
+        L.orc_dit_forward.argtypes = [C.POINTER(DiT), P, P, I, I, I, F, F, P, I]
+        L._models_bound = True
+    return L
+
+
+def tensor(raw: np.ndarray, qtype: int, K: int, N: int, keep: list) -> Tensor:
+    """Wrap raw GGUF bytes (or float32 for F32) of a [K, N] tensor; `keep` holds the buffer."""
+    a = np.ascontiguousarray(raw)
+    keep.append(a)
+    return Tensor(qtype, a.ctypes.data, K, N)
+
+
+class OracleQwen3:
+    """Weights dict (name -> (qtype, raw ndarray, K, N)) following the reference's tensor names
+    after fusion: embed, final_norm, layers.{i}.{attn_norm,qkv,q_norm,k_norm,o,post_norm,gate_up,down}."""
+
+    def __init__(self, cfg: dict, weights: dict):
+        self.keep = []
+        self.cfg = cfg
+        L = cfg["n_layers"]
+        self.layers = (Qwen3Layer * L)()
+        for i in range(L):
+            for f in Qwen3Layer._fields_:
+                qt, raw, K, N = weights[f"layers.{i}.{f[0]}"]
+                setattr(self.layers[i], f[0], tensor(raw, qt, K, N, self.keep))
+        qt, raw, K, N = weights["embed"]
+        emb = tensor(raw, qt, K, N, self.keep)
+        qt, raw, K, N = weights["final_norm"]
+        fn = tensor(raw, qt, K, N, self.keep)
+        self.m = Qwen3(L, cfg["H"], cfg["F"], cfg["Nh"], cfg["Nkv"], cfg["D"], cfg["V"], cfg["rope_theta"],
+                       cfg["eps"], emb, fn, self.layers)
+        self.kv = None
+
+    def encode(self, ids):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty((ids.size, self.cfg["H"]), dtype=np.float32)
+        rc = _models_lib().orc_qwen3_encode(C.byref(self.m), _p(ids), ids.size, _p(out))
+        assert rc == 0
+        return out
+
+    def alloc_kv(self, n_sets: int, max_seq: int):
+        c = self.cfg
+        shape = (c["n_layers"], n_sets, c["Nkv"], max_seq, c["D"])
+        self.kbuf = np.zeros(shape, dtype=np.uint16)
+        self.vbuf = np.zeros(shape, dtype=np.uint16)
+        self.kv = KV(self.kbuf.ctypes.data, self.vbuf.ctypes.data, n_sets, max_seq)
+        self.kv_pos = [0] * n_sets
+
+    def prefill(self, ids, set_=0, lm_offset=0, lm_count=0, want_hidden=False):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        V = lm_count if lm_count > 0 else self.cfg["V"]
+        logits = np.empty(V, dtype=np.float32)
+        hid = np.empty((ids.size, self.cfg["H"]), dtype=np.float32) if want_hidden else None
+        rc = _models_lib().orc_qw3lm_prefill(C.byref(self.m), C.byref(self.kv), set_, self.kv_pos[set_], _p(ids),
+                                             ids.size, _p(logits), lm_offset, lm_count, _p(hid))
+        assert rc == 0
+        self.kv_pos[set_] += ids.size
+        return (logits, hid) if want_hidden else logits
+
+    def decode(self, ids, set0=0, lm_offset=0, lm_count=0):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        N = ids.size
+        pos = np.array(self.kv_pos[set0:set0 + N], dtype=np.int32)
+        V = lm_count if lm_count > 0 else self.cfg["V"]
+        logits = np.empty((N, V), dtype=np.float32)
+        rc = _models_lib().orc_qw3lm_decode(C.byref(self.m), C.byref(self.kv), set0, _p(pos), _p(ids), N,
+                                            _p(logits), lm_offset, lm_count)
+        assert rc == 0
+        for i in range(N):
+            self.kv_pos[set0 + i] += 1
+        return logits
+
+
+class OracleDiT:
+    """Weights dict (name -> (qtype, raw, K, N)) with names te.*, te_r.*, proj_in_w, proj_in_b,
+    cond_w, cond_b, layers.{i}.<DiTLayer field>, norm_out, out_ss, proj_out_w, proj_out_b."""
+
+    def __init__(self, cfg: dict, weights: dict):
+        self.keep = []
+        self.cfg = cfg
+        L = cfg["n_layers"]
+        self.layers = (DiTLayer * L)()
+        for i in range(L):
+            for f in DiTLayer._fields_[:-1]:
+                qt, raw, K, N = weights[f"layers.{i}.{f[0]}"]
+                setattr(self.layers[i], f[0], tensor(raw, qt, K, N, self.keep))
+            self.layers[i].layer_type = 0 if i % 2 == 0 else 1
+
+        def T(name):
+            qt, raw, K, N = weights[name]
+            return tensor(raw, qt, K, N, self.keep)
+
+        te = DiTTemb(*[T(f"te.{n}") for n, _ in DiTTemb._fields_])
+        te_r = DiTTemb(*[T(f"te_r.{n}") for n, _ in DiTTemb._fields_])
+        self.m = DiT(L, cfg["H"], cfg["F"], cfg["Nh"], cfg["Nkv"], cfg["D"], cfg["in_ch"], cfg["out_ch"], cfg["P"],
+                     cfg["sliding_window"], cfg["H_enc"], cfg["rope_theta"], cfg["eps"], te, te_r,
+                     T("proj_in_w"), T("proj_in_b"), T("cond_w"), T("cond_b"), self.layers, T("norm_out"),
+                     T("out_ss"), T("proj_out_w"), T("proj_out_b"))
+
+    def forward(self, x, enc, t, t_r, n_layers_run=-1):
+        x = _f32(x)
+        enc = _f32(enc)
+        N, T_, _ = x.shape
+        enc_S = enc.shape[1]
+        out = np.empty((N, T_, self.cfg["out_ch"]), dtype=np.float32)
+        rc = _models_lib().orc_dit_forward(C.byref(self.m), _p(x), _p(enc), N, T_, enc_S, t, t_r, _p(out),
+                                           n_layers_run)
+        assert rc == 0
+        return out
