@@ -333,6 +333,7 @@ def run_ours(args):
         per_op[f"{name}.{io}"] = {"ms": statistics.mean(d), "GB/s": b / (statistics.mean(d) * 1e-3) / 1e9,
                                   "bytes": b}
     value = ws * step_bytes * args.steps / (ms * 1e-3) / 1e9
+    n_launch = len(ops) * args.steps
 
     # e2e through the C ABI with host buffers (pinned), copies inside the timed region
     for w in wls:
@@ -371,6 +372,12 @@ def run_ours(args):
         cpu = {"value": round(v, 3), "unit": "GB/s", "cores": info["cores"], "kind": "port",
                "sample": info["sample"]}
 
+    lm = None
+    if "lm" in args.workloads.split(",") and ws == 1:
+        del wls, ops, evs
+        torch.cuda.empty_cache()
+        lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline)
+
     if rank == 0:
         line = {"metric": "fused-op HBM GB/s (config 2 op-chain, algorithmic bytes)", "value": round(value, 2),
                 "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
@@ -387,7 +394,7 @@ def run_ours(args):
                                              for k, v in per_op.items()},
                 "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-                "gpu_launches": len(ops) * args.steps, "clocks": clocks, "cpu_baseline": cpu}
+                "gpu_launches": n_launch, "clocks": clocks, "cpu_baseline": cpu, "lm_decode": lm}
         print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()
@@ -397,6 +404,134 @@ def run_ours(args):
 TRAFFIC: dict = {}
 
 
+# ---- workload: BASELINE config 3 (Qwen3-1.7B-shaped LM, greedy decode, batch 1) ----------------
+
+LM_PROMPT, LM_GEN = 512, 1024
+
+
+def lm_weight_bytes(cfg) -> int:
+    """Weight bytes streamed per decoded token (every linear + the tied head), Q8_0."""
+    H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
+    Nh, Nkv, D, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"], cfg["vocab_size"]
+    q8 = lambda n, k: n * (k // 32) * 34
+    per_layer = q8((Nh + 2 * Nkv) * D, H) + q8(H, Nh * D) + q8(2 * F, H) + q8(H, F) + (2 * H + 2 * D) * 4
+    return L * per_layer + q8(V, H) + H * 4
+
+
+def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None):
+    """Config 3 on this GPU: returns the lm_decode result dict."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+    import synthetic
+
+    cfg = dict(synthetic.QWEN3_1_7B)
+    d = gguf_dir or tempfile.gettempdir()
+    path = os.path.join(d, f"acb_bench_lm17_q8_0_r{rank}.gguf")
+    keep = {} if want_cpu else None
+    t0 = time.time()
+    synthetic.write_lm_gguf(path, cfg, synthetic.policy_q8_0, seed=42, device=str(dev), keep=keep)
+    t_gen = time.time() - t0
+    m = acb.QW3LM(path, max_seq_len=8192, n_kv_sets=1, device=dev.index or 0)
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(0, cfg["vocab_size"], size=LM_PROMPT).astype(np.int32)
+    t0 = time.time()
+    lg = m.forward(prompt, kv_set=0)
+    t_prefill = time.time() - t0
+    first = int(np.argmax(lg))
+    # warm-up (captures the step graph), then the timed stretch of the 1024 generated tokens
+    toks_w, _, _ = m.generate_greedy([first], 0, warm_tokens)
+    n_timed = LM_GEN - warm_tokens
+    toks, _, gpu_ms = m.generate_greedy([int(toks_w[0, -1])], 0, n_timed)
+    tok_s = n_timed / (gpu_ms * 1e-3)
+    wb = lm_weight_bytes(cfg)
+    # KV bytes read per token at the average context of the timed stretch (K and V, f16)
+    avg_ctx = LM_PROMPT + warm_tokens + n_timed / 2
+    kv_b = int(avg_ctx * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * 2 * 2)
+    per_tok_bytes = wb + kv_b
+    # e2e through the reference-facing API: host ids in, host logits out, host argmax
+    nxt = int(toks[0, -1])
+    e2e_n = 32
+    t0 = time.perf_counter()
+    for _ in range(e2e_n):
+        lg = m.forward_batch(np.array([nxt], np.int32), [0])
+        nxt = int(np.argmax(lg[0]))
+    e2e_s = time.perf_counter() - t0
+    V = cfg["vocab_size"]
+    # dominant kernel: the head-shaped GEMV (217472 x 2048 Q8_0, M=1), timed alone with events
+    head = torch.randint(0, 256, (V * 2176 + 256,), dtype=torch.uint8, device=dev)
+    head.view(-1)[: V * 2176].view(V, 64, 34)[:, :, 0:2] = torch.tensor([0x00, 0x14], dtype=torch.uint8,
+                                                                        device=dev)  # d = 2^-10 (f16 0x1400)
+    x = torch.randn(1, 2048, device=dev)
+    y = torch.empty(1, V, device=dev)
+    for _ in range(3):
+        acb.gemv(head, acb.Q8_0, V, 2048, x, y=y)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    e0.record()
+    for _ in range(reps):
+        acb.gemv(head, acb.Q8_0, V, 2048, x, y=y)
+    e1.record()
+    torch.cuda.synchronize()
+    head_ms = e0.elapsed_time(e1) / reps
+    head_bytes = V * 2176 + 2048 * 4 + V * 4
+    peaks, kind = measured_peaks()
+    res = {
+        "metric": "LM decode tok/s (config 3: Qwen3-1.7B shape, Q8_0, batch 1, greedy)",
+        "value": round(tok_s, 2), "unit": "tok/s", "higher_is_better": True,
+        "ms_per_token": round(gpu_ms / n_timed, 4),
+        "config": {"workload": "config3_lm17_q8_0_decode", "prompt": LM_PROMPT, "generated": LM_GEN,
+                   "timed_tokens": n_timed, "kv_cache": "f16 max_seq 8192", "weights_MB": round(wb / 1e6, 1),
+                   "setup_s": {"gguf_write": round(t_gen, 1), "prefill": round(t_prefill, 2)}},
+        "hbm": {"bytes_per_token": per_tok_bytes, "achieved_GBs": round(per_tok_bytes * tok_s / 1e9, 1),
+                "frac_of_measured": round(per_tok_bytes * tok_s / 1e9 / peaks["hbm_gbs"], 4),
+                "bound_us_per_token": round(per_tok_bytes / (peaks["hbm_gbs"] * 1e3), 1),
+                "ratio_to_bound": round((gpu_ms / n_timed * 1e3) / (per_tok_bytes / (peaks["hbm_gbs"] * 1e3)), 3)},
+        "roofline": {"kernel": "gemv_kernel<Q8_0,M=1> 217472x2048 (LM-head shape)", "bound": "hbm",
+                     "achieved": round(head_bytes / (head_ms * 1e-3) / 1e9, 1), "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(head_bytes / (head_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                     "traffic": None},
+        "e2e": {"value": round(e2e_n / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": V * 4, "path": "acb_qw3lm_forward_batch + host argmax"},
+        "tokens_head": toks[0, :8].tolist(),
+    }
+    if want_cpu:
+        res["cpu_baseline"] = cpu_lm_sample(cfg, keep, prompt)
+    m.close()
+    del keep
+    try:
+        os.remove(path)
+    except OSError:
+        pass
+    return res
+
+
+def cpu_lm_sample(cfg, keep, prompt, n_prefill=8, n_decode=3):
+    """Oracle decode of the same weights on the host cores (bounded sample: a short prefill,
+    then n_decode timed one-token steps; each step streams every weight like the GPU step)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    tensors = {}
+    for name, (qt, raw, K) in keep.items():
+        N = raw.shape[0] if raw.ndim > 1 else 1
+        tensors[name] = (qt, raw, K, N)
+    m = O.qwen3_from_gguf_tensors(cfg, tensors)
+    m.alloc_kv(1, n_prefill + n_decode + 1)
+    lg = m.prefill(prompt[:n_prefill])
+    nxt = int(np.argmax(lg))
+    t0 = time.perf_counter()
+    for _ in range(n_decode):
+        lg = m.decode(np.array([nxt], np.int32))[0]
+        nxt = int(np.argmax(lg))
+    dt = time.perf_counter() - t0
+    return {"value": round(n_decode / dt, 3), "unit": "tok/s", "cores": O.get_threads(), "kind": "port",
+            "sample": f"oracle decode, {n_decode} tokens after an {n_prefill}-token prefill, same Q8_0 weights"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -404,6 +539,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workloads", default="ops,lm",
+                    help="comma list: ops (config 2, the headline line), lm (config 3 decode, N=1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -65,6 +65,30 @@ def lib():
             "acb_adaln_modulate": (I, [P, I, P, F, P, P, I64, P, I, I64, I64, I, P]),
             "acb_gated_residual": (I, [P, P, I, P, I64, P, I64, I64, I, P]),
             "acb_get_rows": (I, [P, I, I64, I64, P, I64, P, I, I64, P, P]),
+            "acb_quantize": (I, [P, I64, I64, I, P, P]),
+            "acb_gemv": (I, [P, I, I64, I64, I, I, P, I64, P, F, I, P, I64, I, P, I64, I, P, P]),
+            "acb_qkv_post": (I, [P, I64, I64, I, I, I, P, P, F, P, P, I, P, I64, P, P, I, I, I, I, P, P]),
+            "acb_attn_decode_splits": (I, [I, I]),
+            "acb_attn_decode": (I, [P, I64, I, I, I, I, P, P, P, I, I, I, F, I, P, P, P, I, P]),
+            "acb_argmax": (I, [P, I64, I64, I, P, P, P, P, P, I64, P, I, P]),
+            # model level (acb_models.h)
+            "acb_last_error": (C.c_char_p, []),
+            "acb_gguf_open": (I, [C.c_char_p, C.POINTER(C.c_void_p)]),
+            "acb_gguf_close": (None, [P]),
+            "acb_gguf_n_tensors": (I64, [P]),
+            "acb_gguf_find_tensor": (I64, [P, C.c_char_p]),
+            "acb_gguf_get_u32": (C.c_uint32, [P, C.c_char_p]),
+            "acb_gguf_get_str": (C.c_char_p, [P, C.c_char_p]),
+            "acb_qw3lm_load": (I, [C.c_char_p, I, I, I, C.POINTER(C.c_void_p)]),
+            "acb_qw3lm_forward": (I, [P, P, I, I, P]),
+            "acb_qw3lm_forward_batch": (I, [P, P, P, I, P, I, I]),
+            "acb_qw3lm_reset_kv": (None, [P, I]),
+            "acb_qw3lm_copy_kv": (I, [P, I, I]),
+            "acb_qw3lm_build_partial_head": (I, [P, I]),
+            "acb_qw3lm_kv_pos": (I, [P, I]),
+            "acb_qw3lm_weight_bytes": (C.c_size_t, [P]),
+            "acb_qw3lm_generate_greedy": (I, [P, P, I, I, I, P, P, P]),
+            "acb_qw3lm_free": (None, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -183,3 +207,131 @@ def get_rows(table, table_type, n_rows, cols, ids, out=None, out_dtype=None, err
     _check("acb_get_rows", lib().acb_get_rows(_ptr(table), table_type, n_rows, cols, _ptr(ids), n, _ptr(out),
                                                dtype_id(out), out.stride(0), _ptr(err), _stream(stream)))
     return out
+
+
+# ---- decode path -------------------------------------------------------------------------------
+
+PRO_X, PRO_RMSNORM, PRO_SUM_SPLITS, PRO_SWIGLU = 0, 1, 2, 3
+EPI_STORE, EPI_ADD = 0, 1
+FLAG_PDL = 1
+
+
+def gemv(W, w_type, N, K, x, M=None, prologue=PRO_X, x_stride=None, norm_w=None, eps=1e-6, n_split=1, y=None,
+         y_stride=None, epilogue=EPI_STORE, res=None, res_stride=None, flags=0, err=None, stream=None):
+    """y[m][n] = W[n] . act(x)[m]; W raw GGUF rows (uint8 device tensor or pointer)."""
+    import torch
+    if M is None:
+        M = x.shape[0] if x.dim() > 1 else 1
+    xs = x_stride if x_stride is not None else (x.stride(0) if x.dim() > 1 else K)
+    if y is None:
+        y = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    ys = y_stride if y_stride is not None else (y.stride(0) if y.dim() > 1 else N)
+    rs = res_stride if res_stride is not None else (res.stride(0) if res is not None and res.dim() > 1 else N)
+    _check("acb_gemv", lib().acb_gemv(_ptr(W), w_type, N, K, M, prologue, _ptr(x), xs, _ptr(norm_w), eps, n_split,
+                                       _ptr(y), ys, epilogue, _ptr(res), rs, flags, _ptr(err), _stream(stream)))
+    return y
+
+
+def qkv_post(qkv, n_tok, Nh, Nkv, D, q_norm, k_norm, eps, pos, rope, q_out, k_cache, v_cache, max_seq, set0,
+             set_per_tok, flags=0, err=None, stream=None):
+    _check("acb_qkv_post", lib().acb_qkv_post(
+        _ptr(qkv), qkv.stride(0), n_tok, Nh, Nkv, D, _ptr(q_norm), _ptr(k_norm), eps, _ptr(pos), _ptr(rope),
+        rope.shape[0], _ptr(q_out), q_out.stride(0), _ptr(k_cache), _ptr(v_cache), max_seq, set0, set_per_tok,
+        flags, _ptr(err), _stream(stream)))
+
+
+def attn_decode_splits(n_tok, Nkv):
+    return lib().acb_attn_decode_splits(n_tok, Nkv)
+
+
+def attn_decode(q, n_tok, Nh, Nkv, D, pos, k_cache, v_cache, max_seq, set0, set_per_tok, scale, n_split, scores,
+                smax, part, flags=0, stream=None):
+    _check("acb_attn_decode", lib().acb_attn_decode(
+        _ptr(q), q.stride(0), n_tok, Nh, Nkv, D, _ptr(pos), _ptr(k_cache), _ptr(v_cache), max_seq, set0, set_per_tok,
+        scale, n_split, _ptr(scores), _ptr(smax), _ptr(part), flags, _stream(stream)))
+
+
+def argmax(logits, ids, margin=None, pos_advance=None, flags=0, stream=None):
+    rows, V = logits.shape
+    _check("acb_argmax", lib().acb_argmax(_ptr(logits), logits.stride(0), V, rows, _ptr(ids), _ptr(margin),
+                                           _ptr(pos_advance), None, None, 0, None, flags, _stream(stream)))
+
+
+# ---- model level ----------------------------------------------------------------------------------
+
+class QW3LM:
+    """Qwen3 causal LM (acb_models.h): the qw3lm_* entry points of src/qwen3-lm.h."""
+
+    def __init__(self, gguf_path: str, max_seq_len: int = 0, n_kv_sets: int = 1, device: int = 0):
+        import numpy as np
+        self.np = np
+        h = C.c_void_p()
+        st = lib().acb_qw3lm_load(gguf_path.encode(), max_seq_len, n_kv_sets, device, C.byref(h))
+        if st != 0:
+            raise AcbError(f"acb_qw3lm_load ({lib().acb_last_error().decode()})", st)
+        self.h = h
+        self.cfg = self._config()
+
+    def _config(self):
+        fields = ["vocab_size", "hidden_size", "intermediate_size", "n_heads", "n_kv_heads", "head_dim",
+                  "n_layers", "rope_theta", "rms_norm_eps", "tie_embeddings", "max_seq_len"]
+
+        class Cfg(C.Structure):
+            _fields_ = [(f, C.c_float if f in ("rope_theta", "rms_norm_eps") else C.c_int) for f in fields]
+        c = Cfg()
+        fn = lib().acb_qw3lm_get_config
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.POINTER(Cfg)]
+        _check("acb_qw3lm_get_config", fn(self.h, C.byref(c)))
+        return {f: getattr(c, f) for f in fields}
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().acb_qw3lm_free(self.h)
+            self.h = None
+
+    __del__ = close
+
+    def weight_bytes(self) -> int:
+        return lib().acb_qw3lm_weight_bytes(self.h)
+
+    def kv_pos(self, s=0) -> int:
+        return lib().acb_qw3lm_kv_pos(self.h, s)
+
+    def reset_kv(self, s=0):
+        lib().acb_qw3lm_reset_kv(self.h, s)
+
+    def copy_kv(self, src, dst):
+        _check("acb_qw3lm_copy_kv", lib().acb_qw3lm_copy_kv(self.h, src, dst))
+
+    def build_partial_head(self, lm_offset):
+        _check("acb_qw3lm_build_partial_head", lib().acb_qw3lm_build_partial_head(self.h, lm_offset))
+
+    def forward(self, ids, kv_set=0):
+        np = self.np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty(self.cfg["vocab_size"], dtype=np.float32)
+        _check("acb_qw3lm_forward", lib().acb_qw3lm_forward(self.h, ids.ctypes.data, ids.size, kv_set,
+                                                             out.ctypes.data))
+        return out
+
+    def forward_batch(self, ids, kv_sets, lm_offset=0, lm_count=0, out_v=None):
+        np = self.np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        sets = np.ascontiguousarray(kv_sets, dtype=np.int32)
+        V = out_v or (lm_count if lm_count > 0 else self.cfg["vocab_size"])
+        out = np.empty((ids.size, V), dtype=np.float32)
+        _check("acb_qw3lm_forward_batch", lib().acb_qw3lm_forward_batch(
+            self.h, ids.ctypes.data, sets.ctypes.data, ids.size, out.ctypes.data, lm_offset, lm_count))
+        return out
+
+    def generate_greedy(self, last_ids, set0, n_steps, want_margins=False):
+        np = self.np
+        last = np.ascontiguousarray(last_ids, dtype=np.int32)
+        N = last.size
+        toks = np.empty((N, n_steps), dtype=np.int32)
+        marg = np.empty((N, n_steps), dtype=np.float32) if want_margins else None
+        ms = C.c_float(0.0)
+        _check("acb_qw3lm_generate_greedy", lib().acb_qw3lm_generate_greedy(
+            self.h, last.ctypes.data, set0, N, n_steps, toks.ctypes.data,
+            None if marg is None else marg.ctypes.data, C.byref(ms)))
+        return toks, marg, ms.value

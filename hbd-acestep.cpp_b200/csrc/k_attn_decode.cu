@@ -1,0 +1,479 @@
+// k_attn_decode.cu -- the attention part of one batched decode step (qw3lm_forward_batch,
+// src/qwen3-lm.h:633-733): fused QKV post-processing into the f16 KV cache, split-KV attention
+// over the cache, and the greedy argmax that feeds the next step's embedding gather.
+//
+// Attention reproduces ggml-CPU's qwen3_attn_f32 on an f16 cache (src/qwen3-enc.h:101-112):
+//   s_j = (f16(q) . k_j) * scale                 f32 accumulation
+//   p_j = f16( expf(s_j - max) * (float)(1/sum) ) sum of expf in double
+//   o   = sum_j p_j v_j                           f32 accumulation
+// The normalised probabilities are rounded before the PV product, so the step runs in two
+// passes over split chunks of the cache: pass 1 writes scores and per-split maxima, pass 2
+// normalises and forms per-split partial outputs; the O-projection GEMV sums the partials in
+// its prologue. Every CTA of a head computes the same global sum in the same order, so all
+// splits use identical normalisers.
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace acb {
+
+struct KvLayout {
+    uint16_t * k;  // f16 cache [n_sets][Nkv][max_seq][D]
+    uint16_t * v;
+    int        max_seq;
+    int        set0;
+    int        set_per_tok;  // token i uses set set0 + i*set_per_tok
+};
+
+__device__ __forceinline__ int64_t kv_index(const KvLayout & kv, int Nkv, int D, int set, int h, int p) {
+    return (((int64_t) set * Nkv + h) * kv.max_seq + p) * D;
+}
+
+template <int PDL>
+__device__ __forceinline__ void dep_wait() {
+    if (PDL) {
+        ptx::grid_dep_wait();
+    }
+}
+
+// ---- fused QKV post: q -> norm+rope -> q_out (f32); k -> norm+rope -> cache; v -> cache -------
+// one warp per (token, head of Nh + 2 Nkv); D = 128 (E = 2 elements per lane per half)
+template <int E, int PDL>
+__global__ void __launch_bounds__(256) qkv_post_kernel(const float * __restrict__ qkv, int64_t qkv_stride,
+                                                       int64_t n_tok, int Nh, int Nkv,
+                                                       const float * __restrict__ q_norm,
+                                                       const float * __restrict__ k_norm, float eps,
+                                                       const int32_t * __restrict__ pos,
+                                                       const float * __restrict__ rope, int max_pos,
+                                                       float * __restrict__ q_out, int64_t q_stride, KvLayout kv,
+                                                       int * __restrict__ err) {
+    constexpr int D    = 64 * E;
+    constexpr int HALF = D / 2;
+    dep_wait<PDL>();
+    ptx::grid_dep_launch();
+    const int     lane  = threadIdx.x & 31;
+    const int     nh    = Nh + 2 * Nkv;
+    const int64_t item  = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= n_tok * nh) {
+        return;
+    }
+    const int64_t t = item / nh;
+    const int     h = (int) (item - t * nh);
+    const int     p = __ldg(pos + t);
+    if (p < 0 || p >= max_pos || p >= kv.max_seq) {
+        if (lane == 0 && err) {
+            atomicOr(err, ACB_DEVERR_POS_RANGE);
+        }
+        return;
+    }
+    const float * s = qkv + t * qkv_stride + (int64_t) h * D + lane * E;
+    float         a[E], b[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        a[e] = s[e];
+        b[e] = s[HALF + e];
+    }
+    const int     kind = h < Nh ? 0 : (h < Nh + Nkv ? 1 : 2);
+    const float * w    = kind == 0 ? q_norm : k_norm;
+    if (kind < 2) {
+        if (w) {
+            double ss = 0.0;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                ss += (double) __fmul_rn(a[e], a[e]);
+                ss += (double) __fmul_rn(b[e], b[e]);
+            }
+            ss             = warp_sum(ss);
+            const float sc = rms_scale(ss, D, eps);
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * E + e));
+                b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(w + HALF + lane * E + e));
+            }
+        }
+        const float * c = rope + (int64_t) p * D + 2 * lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            const float cs = __ldg(c + 2 * e), sn = __ldg(c + 2 * e + 1);
+            const float x0 = a[e], x1 = b[e];
+            a[e]           = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+            b[e]           = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+        }
+    }
+    if (kind == 0) {
+        float * d = q_out + t * q_stride + (int64_t) h * D + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            d[e]        = a[e];
+            d[HALF + e] = b[e];
+        }
+    } else {
+        const int  set = kv.set0 + (int) t * kv.set_per_tok;
+        const int  hk  = kind == 1 ? h - Nh : h - Nh - Nkv;
+        uint16_t * d   = (kind == 1 ? kv.k : kv.v) + kv_index(kv, Nkv, D, set, hk, p) + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            d[e]        = __half_as_ushort(__float2half_rn(a[e]));
+            d[HALF + e] = __half_as_ushort(__float2half_rn(b[e]));
+        }
+    }
+}
+
+// ---- pass 1: scores of one (token, kv head, split) for the G q heads of the group ---------------
+// block = 128 threads (4 warps); lane owns 4 of the 128 head elements; one key per warp step.
+template <int G, int PDL>
+__global__ void __launch_bounds__(128) attn_scores_kernel(const float * __restrict__ q, int64_t q_stride, int Nh,
+                                                          int Nkv, const int32_t * __restrict__ pos, KvLayout kv,
+                                                          float scale, int n_split, float * __restrict__ scores,
+                                                          int64_t s_stride, float * __restrict__ smax) {
+    constexpr int D = 128;
+    dep_wait<PDL>();
+    ptx::grid_dep_launch();
+    const int   split = blockIdx.x, hk = blockIdx.y, t = blockIdx.z;
+    const int   lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int   kv_len = __ldg(pos + t) + 1;
+    if (kv_len <= 0 || kv_len > kv.max_seq) {
+        return;  // position out of range: acb_qkv_post has already flagged it
+    }
+    const int   chunk  = (kv_len + n_split - 1) / n_split;
+    const int   j0     = split * chunk;
+    const int   j1     = min(kv_len, j0 + chunk);
+    const int   set    = kv.set0 + t * kv.set_per_tok;
+    __shared__ float wmax[4][G];
+    // q of the group's heads, rounded to f16 (the vec-dot type of the f16 cache)
+    float qv[G][4];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float4 v = *reinterpret_cast<const float4 *>(q + (int64_t) t * q_stride + (int64_t) (hk * G + g) * D +
+                                                           lane * 4);
+        qv[g][0]       = __half2float(__float2half_rn(v.x));
+        qv[g][1]       = __half2float(__float2half_rn(v.y));
+        qv[g][2]       = __half2float(__float2half_rn(v.z));
+        qv[g][3]       = __half2float(__float2half_rn(v.w));
+    }
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        mx[g] = -INFINITY;
+    }
+    const uint16_t * kb = kv.k + kv_index(kv, Nkv, D, set, hk, 0);
+    for (int j = j0 + warp; j < j1; j += 4) {
+        const uint2    raw = *reinterpret_cast<const uint2 *>(kb + (int64_t) j * D + lane * 4);
+        const __half2  k01 = *reinterpret_cast<const __half2 *>(&raw.x);
+        const __half2  k23 = *reinterpret_cast<const __half2 *>(&raw.y);
+        const float2   f01 = __half22float2(k01), f23 = __half22float2(k23);
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float acc = __fmul_rn(f01.x, qv[g][0]);
+            acc       = __fadd_rn(acc, __fmul_rn(f01.y, qv[g][1]));
+            acc       = __fadd_rn(acc, __fmul_rn(f23.x, qv[g][2]));
+            acc       = __fadd_rn(acc, __fmul_rn(f23.y, qv[g][3]));
+            acc       = warp_sum(acc);
+            const float sv = __fmul_rn(acc, scale);
+            if (lane == 0) {
+                scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j] = sv;
+            }
+            mx[g] = fmaxf(mx[g], sv);
+        }
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            wmax[warp][g] = mx[g];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int g = threadIdx.x;
+        float     m = fmaxf(fmaxf(wmax[0][g], wmax[1][g]), fmaxf(wmax[2][g], wmax[3][g]));
+        smax[((int64_t) t * Nh + hk * G + g) * n_split + split] = m;
+    }
+}
+
+// ---- pass 2: global normaliser, f16 probabilities of this split's chunk, partial P.V ----------
+template <int G, int PDL>
+__global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__ scores, int64_t s_stride,
+                                                      const float * __restrict__ smax, int Nh, int Nkv,
+                                                      const int32_t * __restrict__ pos, KvLayout kv, int n_split,
+                                                      float * __restrict__ part) {
+    constexpr int D = 128;
+    dep_wait<PDL>();
+    ptx::grid_dep_launch();
+    const int split = blockIdx.x, hk = blockIdx.y, t = blockIdx.z;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int kv_len = __ldg(pos + t) + 1;
+    if (kv_len <= 0 || kv_len > kv.max_seq) {
+        return;
+    }
+    const int chunk  = (kv_len + n_split - 1) / n_split;
+    const int j0     = split * chunk;
+    const int j1     = min(kv_len, j0 + chunk);
+    const int set    = kv.set0 + t * kv.set_per_tok;
+    __shared__ double red[4][G];
+    __shared__ float  sM[G], sInv[G];
+
+    // global max and sum of expf(s - max) over the whole row, in a fixed order
+    float M[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float * sm = smax + ((int64_t) t * Nh + hk * G + g) * n_split;
+        float         m  = -INFINITY;
+        for (int i = 0; i < n_split; i++) {
+            m = fmaxf(m, sm[i]);
+        }
+        M[g] = m;
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float * sr = scores + (int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride;
+        double        s  = 0.0;
+        for (int j = threadIdx.x; j < kv_len; j += 128) {
+            s += (double) expf(__fsub_rn(sr[j], M[g]));
+        }
+        s = warp_sum(s);
+        if (lane == 0) {
+            red[warp][g] = s;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int    g = threadIdx.x;
+        const double S = (red[0][g] + red[1][g]) + (red[2][g] + red[3][g]);
+        sM[g]          = M[g];
+        sInv[g]        = S > 0.0 ? (float) (1.0 / S) : 0.0f;
+    }
+    __syncthreads();
+
+    // partial output over this chunk: lane owns 4 of the D elements, warps split the keys
+    float acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            acc[g][e] = 0.0f;
+        }
+    }
+    const uint16_t * vb = kv.v + kv_index(kv, Nkv, D, set, hk, 0);
+    for (int j = j0 + warp; j < j1; j += 4) {
+        const uint2   raw = *reinterpret_cast<const uint2 *>(vb + (int64_t) j * D + lane * 4);
+        const float2  f01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+        const float2  f23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float sv = scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j];
+            const float pe = __fmul_rn(expf(__fsub_rn(sv, sM[g])), sInv[g]);
+            const float pp = __half2float(__float2half_rn(pe));
+            acc[g][0]      = __fadd_rn(acc[g][0], __fmul_rn(f01.x, pp));
+            acc[g][1]      = __fadd_rn(acc[g][1], __fmul_rn(f01.y, pp));
+            acc[g][2]      = __fadd_rn(acc[g][2], __fmul_rn(f23.x, pp));
+            acc[g][3]      = __fadd_rn(acc[g][3], __fmul_rn(f23.y, pp));
+        }
+    }
+    // reduce the 4 warps through shared memory, then write the split partial [t][split][Nh*D]
+    __shared__ float4 wacc[4][G][32];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        wacc[warp][g][lane] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    }
+    __syncthreads();
+    if (warp < G) {
+        const int g = warp;
+        float4    r = wacc[0][g][lane];
+#pragma unroll
+        for (int w = 1; w < 4; w++) {
+            const float4 o = wacc[w][g][lane];
+            r.x            = __fadd_rn(r.x, o.x);
+            r.y            = __fadd_rn(r.y, o.y);
+            r.z            = __fadd_rn(r.z, o.z);
+            r.w            = __fadd_rn(r.w, o.w);
+        }
+        float4 * dst = reinterpret_cast<float4 *>(part + ((int64_t) t * n_split + split) * Nh * D +
+                                                  (int64_t) (hk * G + g) * D + lane * 4);
+        *dst         = r;
+    }
+}
+
+// ---- greedy argmax over logits rows; optionally advances positions for the next step --------
+template <int PDL>
+__global__ void __launch_bounds__(1024) argmax_kernel(const float * __restrict__ logits, int64_t stride, int64_t V,
+                                                      int32_t * __restrict__ ids, float * __restrict__ margin,
+                                                      int32_t * __restrict__ pos_advance,
+                                                      int32_t * __restrict__ hist, float * __restrict__ mhist,
+                                                      int64_t hist_stride, const int32_t * __restrict__ hist_base) {
+    dep_wait<PDL>();
+    ptx::grid_dep_launch();
+    const int     row = blockIdx.x;
+    const float * l   = logits + (int64_t) row * stride;
+    float         b1 = -INFINITY, b2 = -INFINITY;
+    int           i1 = 0x7fffffff;
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = l[i];
+        if (v > b1) {
+            b2 = b1;
+            b1 = v;
+            i1 = (int) i;
+        } else if (v > b2) {
+            b2 = v;
+        }
+    }
+    __shared__ float sb1[32], sb2[32];
+    __shared__ int   si1[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o);
+        const float ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const int   oi  = __shfl_xor_sync(0xffffffffu, i1, o);
+        if (ob1 > b1 || (ob1 == b1 && oi < i1)) {
+            b2 = fmaxf(b1, ob2);
+            b1 = ob1;
+            i1 = oi;
+        } else {
+            b2 = fmaxf(b2, ob1);
+        }
+    }
+    if (lane == 0) {
+        sb1[warp] = b1;
+        sb2[warp] = b2;
+        si1[warp] = i1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int nw = blockDim.x >> 5;
+        float     B1 = sb1[0], B2 = sb2[0];
+        int       I1 = si1[0];
+        for (int w = 1; w < nw; w++) {
+            if (sb1[w] > B1 || (sb1[w] == B1 && si1[w] < I1)) {
+                B2 = fmaxf(B1, sb2[w]);
+                B1 = sb1[w];
+                I1 = si1[w];
+            } else {
+                B2 = fmaxf(B2, sb1[w]);
+            }
+        }
+        ids[row] = I1;
+        if (margin) {
+            margin[row] = B1 - B2;
+        }
+        if (pos_advance) {
+            if (hist && hist_base) {
+                const int64_t step = pos_advance[row] - hist_base[row];
+                hist[row * hist_stride + step] = I1;
+                if (mhist) {
+                    mhist[row * hist_stride + step] = B1 - B2;
+                }
+            }
+            pos_advance[row] += 1;
+        }
+    }
+}
+
+template <typename Kern, typename... Args>
+static acb_status launch_ex(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = grid;
+    cfg.blockDim           = block;
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = pdl ? attr : nullptr;
+    cfg.numAttrs                                       = pdl ? 1 : 0;
+    cudaError_t e                                      = cudaLaunchKernelEx(&cfg, k, args...);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" acb_status acb_qkv_post(const float * qkv, int64_t qkv_stride, int64_t n_tok, int Nh, int Nkv,
+                                   int head_dim, const float * q_norm, const float * k_norm, float eps,
+                                   const int32_t * pos, const float * rope_table, int max_pos, float * q_out,
+                                   int64_t q_stride, uint16_t * k_cache, uint16_t * v_cache, int max_seq, int set0,
+                                   int set_per_tok, int flags, int * err_flag, acb_stream_t stream) {
+    if (!qkv || !pos || !rope_table || !q_out || !k_cache || !v_cache || n_tok < 0 || Nh <= 0 || Nkv <= 0 ||
+        max_pos <= 0 || max_seq <= 0 || set0 < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (head_dim != 128) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (n_tok == 0) {
+        return ACB_OK;
+    }
+    KvLayout      kv    = { k_cache, v_cache, max_seq, set0, set_per_tok };
+    const int64_t items = n_tok * (Nh + 2 * Nkv);
+    const dim3    grid((unsigned) ((items + 7) / 8));
+    const bool    pdl = flags & 1;
+    if (pdl) {
+        return launch_ex(qkv_post_kernel<2, 1>, grid, dim3(256), 0, (cudaStream_t) stream, true, qkv, qkv_stride,
+                         n_tok, Nh, Nkv, q_norm, k_norm, eps, pos, rope_table, max_pos, q_out, q_stride, kv,
+                         err_flag);
+    }
+    return launch_ex(qkv_post_kernel<2, 0>, grid, dim3(256), 0, (cudaStream_t) stream, false, qkv, qkv_stride, n_tok,
+                     Nh, Nkv, q_norm, k_norm, eps, pos, rope_table, max_pos, q_out, q_stride, kv, err_flag);
+}
+
+extern "C" int acb_attn_decode_splits(int n_tok, int Nkv) {
+    const int per = num_sms() / (n_tok * Nkv > 0 ? n_tok * Nkv : 1);
+    return per < 1 ? 1 : (per > 32 ? 32 : per);
+}
+
+extern "C" acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok, int Nh, int Nkv, int head_dim,
+                                      const int32_t * pos, const uint16_t * k_cache, const uint16_t * v_cache,
+                                      int max_seq, int set0, int set_per_tok, float scale, int n_split,
+                                      float * scores, float * smax, float * part, int flags, acb_stream_t stream) {
+    if (!q || !pos || !k_cache || !v_cache || !scores || !smax || !part || n_tok <= 0 || Nh <= 0 || Nkv <= 0 ||
+        n_split < 1 || max_seq <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (head_dim != 128 || Nh % Nkv != 0 || Nh / Nkv > 8) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    KvLayout     kv   = { (uint16_t *) k_cache, (uint16_t *) v_cache, max_seq, set0, set_per_tok };
+    const int    G    = Nh / Nkv;
+    const dim3   grid((unsigned) n_split, (unsigned) Nkv, (unsigned) n_tok);
+    cudaStream_t st   = (cudaStream_t) stream;
+    const bool   pdl  = flags & 1;
+    acb_status   rc   = ACB_OK;
+#define ACB_ATT(GG)                                                                                                \
+    if (G == GG) {                                                                                                 \
+        rc = pdl ? launch_ex(attn_scores_kernel<GG, 1>, grid, dim3(128), 0, st, true, q, q_stride, Nh, Nkv, pos, kv, \
+                             scale, n_split, scores, (int64_t) max_seq, smax)                                      \
+                 : launch_ex(attn_scores_kernel<GG, 0>, grid, dim3(128), 0, st, false, q, q_stride, Nh, Nkv, pos, kv, \
+                             scale, n_split, scores, (int64_t) max_seq, smax);                                     \
+        if (rc != ACB_OK) {                                                                                        \
+            return rc;                                                                                             \
+        }                                                                                                          \
+        return pdl ? launch_ex(attn_pv_kernel<GG, 1>, grid, dim3(128), 0, st, true, (const float *) scores,        \
+                               (int64_t) max_seq, (const float *) smax, Nh, Nkv, pos, kv, n_split, part)           \
+                   : launch_ex(attn_pv_kernel<GG, 0>, grid, dim3(128), 0, st, false, (const float *) scores,       \
+                               (int64_t) max_seq, (const float *) smax, Nh, Nkv, pos, kv, n_split, part);          \
+    }
+    ACB_ATT(1)
+    ACB_ATT(2)
+    ACB_ATT(4)
+    ACB_ATT(8)
+#undef ACB_ATT
+    return ACB_ERR_UNSUPPORTED;
+}
+
+extern "C" acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
+                                 float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
+                                 int64_t hist_stride, const int32_t * hist_base, int flags, acb_stream_t stream) {
+    if (!logits || !ids || V <= 0 || rows <= 0 || stride < V || (hist && (!pos_advance || !hist_base))) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const bool pdl = flags & 1;
+    if (pdl) {
+        return launch_ex(argmax_kernel<1>, dim3((unsigned) rows), dim3(1024), 0, (cudaStream_t) stream, true, logits,
+                         stride, V, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base);
+    }
+    return launch_ex(argmax_kernel<0>, dim3((unsigned) rows), dim3(1024), 0, (cudaStream_t) stream, false, logits,
+                     stride, V, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base);
+}

@@ -1,0 +1,598 @@
+// k_gemv.cu -- weight-streaming GEMV for batch-1..8 decode: y[m][n] = sum_k W[n][k] x[m][k]
+// with W in GGUF Q8_0 / Q4_K / Q6_K blocks (quantised mul_mat of every decode linear,
+// src/qwen3-lm.h:639-651,755).
+//
+// Design (HBM-bound; the weight bytes are the roofline):
+//   - persistent CTAs, one per SM; each owns a contiguous row range and streams it through a
+//     3-4 stage shared-memory ring filled by 1-D bulk copies (TMA engine) issued by a producer
+//     warp; 8 consumer warps compute from shared memory (one output row per warp at a time);
+//   - the activation is quantised inside the kernel exactly like ggml-CPU's quantised mul_mat
+//     (Q8_0 blocks for Q8_0 weights, Q8_K for K-quants), and the dot products are integer
+//     dp4a sums scaled per block, so each block's contribution equals the CPU's;
+//   - fused prologues build the activation from its producer's output (RMSNorm*w, the sum of
+//     attention split partials, or SwiGLU of a gate|up row); the epilogue optionally adds a
+//     residual (ggml_add(hidden, out));
+//   - programmatic dependent launch: weight prefetch is issued before griddepcontrol.wait, so
+//     the next linear's weights stream while the previous kernel drains.
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace acb {
+
+enum { PRO_X = 0, PRO_RMSNORM = 1, PRO_SUM_SPLITS = 2, PRO_SWIGLU = 3 };
+enum { EPI_STORE = 0, EPI_ADD = 1 };
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads       = (kConsumerWarps + 1) * 32;
+
+struct GemvParams {
+    const uint8_t * W;
+    int64_t         N;
+    int             K;
+    int64_t         row_bytes;
+    int             M;
+    int             prologue;
+    const float *   x;
+    int64_t         x_stride;
+    const float *   norm_w;
+    float           eps;
+    int             n_split;
+    float *         y;
+    int64_t         y_stride;
+    int             epilogue;
+    const float *   res;
+    int64_t         res_stride;
+    int             rows_per_cta;  // multiple of align_rows
+    int             chunk_rows;    // rows per pipeline stage
+    int             stage_bytes;   // 16-byte multiple >= chunk_rows * row_bytes
+    int             stages;
+    int *           err;
+};
+
+// ---- activation value of element k of row m under the prologue ------------------------------
+__device__ __forceinline__ float act_value(const GemvParams & p, int m, int k, float sc) {
+    switch (p.prologue) {
+        case PRO_RMSNORM: {
+            const float h = p.x[(int64_t) m * p.x_stride + k];
+            const float v = __fmul_rn(h, sc);
+            return p.norm_w ? __fmul_rn(v, __ldg(p.norm_w + k)) : v;
+        }
+        case PRO_SUM_SPLITS: {
+            const float * b = p.x + (int64_t) m * p.x_stride + k;
+            float         s = b[0];
+            for (int i = 1; i < p.n_split; i++) {
+                s = __fadd_rn(s, b[(int64_t) i * p.K]);
+            }
+            return s;
+        }
+        case PRO_SWIGLU: {
+            const float g = p.x[(int64_t) m * p.x_stride + k];
+            const float u = p.x[(int64_t) m * p.x_stride + p.K + k];
+            return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+        }
+        default:
+            return p.x[(int64_t) m * p.x_stride + k];
+    }
+}
+
+// RMSNorm scale of activation row m (PRO_RMSNORM), computed by the 256 consumer threads.
+__device__ float rms_scale_block(const GemvParams & p, int m, double * red) {
+    const int tid = threadIdx.x;
+    double    ss  = 0.0;
+    for (int k = tid; k < p.K; k += kConsumerWarps * 32) {
+        const float h = p.x[(int64_t) m * p.x_stride + k];
+        ss += (double) __fmul_rn(h, h);
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) {
+        red[tid >> 5] = ss;
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+    double t = 0.0;
+    for (int w = 0; w < kConsumerWarps; w++) {
+        t += red[w];
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+    return rms_scale(t, p.K, p.eps);
+}
+
+// ---- activation quantisers (into shared memory) ----------------------------------------------
+// Q8_0: qs int8 [M][K], d (f16-rounded, as float) [M][K/32]
+__device__ void quantize_q8_0(const GemvParams & p, int8_t * xq, float * xd, double * red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb   = p.K / 32;
+    for (int m = 0; m < p.M; m++) {
+        const float sc = p.prologue == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
+        for (int b = warp; b < nb; b += kConsumerWarps) {
+            const float v    = act_value(p, m, b * 32 + lane, sc);
+            const float amax = warp_max(fabsf(v));
+            const float d    = amax / 127.0f;
+            const float id   = d != 0.0f ? 1.0f / d : 0.0f;
+            xq[(int64_t) m * p.K + b * 32 + lane] = (int8_t) roundf(__fmul_rn(v, id));
+            if (lane == 0) {
+                xd[m * nb + b] = __half2float(__float2half_rn(d));
+            }
+        }
+    }
+}
+
+// Q8_K: qs int8 [M][K], d float [M][K/256], bsums int [M][K/16]
+__device__ void quantize_q8_K(const GemvParams & p, int8_t * xq, float * xd, int * xbs, double * red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nsb  = p.K / 256;
+    for (int m = 0; m < p.M; m++) {
+        const float sc = p.prologue == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
+        for (int sb = warp; sb < nsb; sb += kConsumerWarps) {
+            float v[8];
+            float amax = 0.0f, mx = 0.0f;
+            int   idx  = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                v[j]         = act_value(p, m, sb * 256 + lane * 8 + j, sc);
+                const float a = fabsf(v[j]);
+                if (a > amax) {  // first index of the largest magnitude wins
+                    amax = a;
+                    mx   = v[j];
+                    idx  = lane * 8 + j;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+                const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+                const int   oi = __shfl_xor_sync(0xffffffffu, idx, o);
+                if (oa > amax || (oa == amax && oi < idx)) {
+                    amax = oa;
+                    mx   = om;
+                    idx  = oi;
+                }
+            }
+            int8_t * q = xq + (int64_t) m * p.K + sb * 256 + lane * 8;
+            int      s = 0;
+            if (amax == 0.0f) {
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    q[j] = 0;
+                }
+            } else {
+                const float iscale = -127.0f / mx;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    int iv = __float2int_rn(__fmul_rn(iscale, v[j]));
+                    iv     = iv < 127 ? iv : 127;
+                    q[j]   = (int8_t) iv;
+                    s += iv;
+                }
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);  // lanes 2g, 2g+1 hold group g
+            if ((lane & 1) == 0) {
+                xbs[m * (p.K / 16) + sb * 16 + lane / 2] = s;
+            }
+            if (lane == 0) {
+                xd[m * nsb + sb] = amax == 0.0f ? 0.0f : 1.0f / (-127.0f / mx);
+            }
+        }
+    }
+}
+
+// ---- per-row dot products from a shared-memory weight row ------------------------------------
+template <int MT>
+__device__ __forceinline__ void dot_q8_0(const uint8_t * wrow, const GemvParams & p, const int8_t * xq,
+                                         const float * xd, float * acc) {
+    const int lane = threadIdx.x & 31;
+    const int np   = p.K / 64;  // block pairs (68 bytes, 4-byte aligned)
+    for (int pr = lane; pr < np; pr += 32) {
+        const uint32_t * w32 = reinterpret_cast<const uint32_t *>(wrow + 68 * pr);
+        uint32_t         w[17];
+#pragma unroll
+        for (int j = 0; j < 17; j++) {
+            w[j] = w32[j];
+        }
+        const float d0 = f16_bits_to_f((uint16_t) (w[0] & 0xffff));
+        const float d1 = f16_bits_to_f((uint16_t) (w[8] >> 16));
+        int         q0[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            q0[j] = (int) __byte_perm(w[j], w[j + 1], 0x5432);
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (m < p.M) {
+                const int4 * xv = reinterpret_cast<const int4 *>(xq + (int64_t) m * p.K + 64 * pr);
+                const int4   a = xv[0], b = xv[1], c = xv[2], e = xv[3];
+                int          s0 = 0, s1 = 0;
+                s0 = __dp4a(q0[0], a.x, s0);
+                s0 = __dp4a(q0[1], a.y, s0);
+                s0 = __dp4a(q0[2], a.z, s0);
+                s0 = __dp4a(q0[3], a.w, s0);
+                s0 = __dp4a(q0[4], b.x, s0);
+                s0 = __dp4a(q0[5], b.y, s0);
+                s0 = __dp4a(q0[6], b.z, s0);
+                s0 = __dp4a(q0[7], b.w, s0);
+                s1 = __dp4a((int) w[9], c.x, s1);
+                s1 = __dp4a((int) w[10], c.y, s1);
+                s1 = __dp4a((int) w[11], c.z, s1);
+                s1 = __dp4a((int) w[12], c.w, s1);
+                s1 = __dp4a((int) w[13], e.x, s1);
+                s1 = __dp4a((int) w[14], e.y, s1);
+                s1 = __dp4a((int) w[15], e.z, s1);
+                s1 = __dp4a((int) w[16], e.w, s1);
+                const float * dx = xd + m * (p.K / 32) + 2 * pr;
+                acc[m]           = __fadd_rn(acc[m], __fmul_rn((float) s0, __fmul_rn(d0, dx[0])));
+                acc[m]           = __fadd_rn(acc[m], __fmul_rn((float) s1, __fmul_rn(d1, dx[1])));
+            }
+        }
+    }
+}
+
+// Q4_K: lane = (superblock slot lane/8, sub-block lane%8); the integer sums of the 8 sub-blocks
+// of a superblock are combined exactly before the float scaling.
+template <int MT>
+__device__ __forceinline__ void dot_q4_K(const uint8_t * wrow, const GemvParams & p, const int8_t * xq,
+                                         const float * xd, const int * xbs, float * acc) {
+    const int lane = threadIdx.x & 31;
+    const int sub  = lane & 7;
+    const int nsb  = p.K / 256;
+    for (int sb0 = 0; sb0 < nsb; sb0 += 4) {
+        const int  sb    = sb0 + (lane >> 3);
+        const bool valid = sb < nsb;
+        const uint8_t * blk = wrow + (int64_t) (valid ? sb : 0) * 144;
+        int             scv = 0, mnv = 0;
+        uint32_t        qw[8];
+        float           d = 0.0f, dmin = 0.0f;
+        if (valid) {
+            d                  = f16_bits_to_f(ld_u16(blk));
+            dmin               = f16_bits_to_f(ld_u16(blk + 2));
+            const uint8_t * sc = blk + 4;
+            if (sub < 4) {
+                scv = sc[sub] & 63;
+                mnv = sc[sub + 4] & 63;
+            } else {
+                scv = (sc[sub + 4] & 0x0f) | ((sc[sub - 4] >> 6) << 4);
+                mnv = (sc[sub + 4] >> 4) | ((sc[sub] >> 6) << 4);
+            }
+            const uint4 * q4 = reinterpret_cast<const uint4 *>(blk + 16 + (sub >> 1) * 32);
+            const uint4   u0 = q4[0], u1 = q4[1];
+            const int     sh = 4 * (sub & 1);
+            qw[0]            = (u0.x >> sh) & 0x0F0F0F0Fu;
+            qw[1]            = (u0.y >> sh) & 0x0F0F0F0Fu;
+            qw[2]            = (u0.z >> sh) & 0x0F0F0F0Fu;
+            qw[3]            = (u0.w >> sh) & 0x0F0F0F0Fu;
+            qw[4]            = (u1.x >> sh) & 0x0F0F0F0Fu;
+            qw[5]            = (u1.y >> sh) & 0x0F0F0F0Fu;
+            qw[6]            = (u1.z >> sh) & 0x0F0F0F0Fu;
+            qw[7]            = (u1.w >> sh) & 0x0F0F0F0Fu;
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (m < p.M) {
+                int isum = 0, imin = 0;
+                if (valid) {
+                    const int4 * xv  = reinterpret_cast<const int4 *>(xq + (int64_t) m * p.K + sb * 256 + sub * 32);
+                    const int4   a   = xv[0], b = xv[1];
+                    int          dot = 0;
+                    dot              = __dp4a((int) qw[0], a.x, dot);
+                    dot              = __dp4a((int) qw[1], a.y, dot);
+                    dot              = __dp4a((int) qw[2], a.z, dot);
+                    dot              = __dp4a((int) qw[3], a.w, dot);
+                    dot              = __dp4a((int) qw[4], b.x, dot);
+                    dot              = __dp4a((int) qw[5], b.y, dot);
+                    dot              = __dp4a((int) qw[6], b.z, dot);
+                    dot              = __dp4a((int) qw[7], b.w, dot);
+                    const int * bs   = xbs + m * (p.K / 16) + sb * 16 + 2 * sub;
+                    isum             = scv * dot;
+                    imin             = mnv * (bs[0] + bs[1]);
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    isum += __shfl_xor_sync(0xffffffffu, isum, o);
+                    imin += __shfl_xor_sync(0xffffffffu, imin, o);
+                }
+                if (valid && sub == 0) {
+                    const float dx = xd[m * nsb + sb];
+                    acc[m]         = __fadd_rn(acc[m], __fmul_rn(__fmul_rn(d, dx), (float) isum));
+                    acc[m]         = __fsub_rn(acc[m], __fmul_rn(__fmul_rn(dmin, dx), (float) imin));
+                }
+            }
+        }
+    }
+}
+
+// Q6_K: lane = (superblock slot lane/16, 16-element group lane%16). Unsigned 6-bit values are
+// dotted and the -32 offset removed with the activation's 16-element sum (exact integers).
+template <int MT>
+__device__ __forceinline__ void dot_q6_K(const uint8_t * wrow, const GemvParams & p, const int8_t * xq,
+                                         const float * xd, const int * xbs, float * acc) {
+    const int lane = threadIdx.x & 31;
+    const int g    = lane & 15;
+    const int nsb  = p.K / 256;
+    const int half = g >> 3, c = (g >> 1) & 3, l0 = (g & 1) * 16;
+    for (int sb0 = 0; sb0 < nsb; sb0 += 2) {
+        const int       sb    = sb0 + (lane >> 4);
+        const bool      valid = sb < nsb;
+        const uint8_t * blk   = wrow + (int64_t) (valid ? sb : 0) * 210;
+        uint32_t        vw[4];
+        int             scv = 0;
+        float           d   = 0.0f;
+        if (valid) {
+            const uint16_t * ql = reinterpret_cast<const uint16_t *>(blk + half * 64 + (c & 1) * 32 + l0);
+            const uint16_t * qh = reinterpret_cast<const uint16_t *>(blk + 128 + half * 32 + l0);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t lo4 = (uint32_t) ql[2 * j] | ((uint32_t) ql[2 * j + 1] << 16);
+                const uint32_t hi4 = (uint32_t) qh[2 * j] | ((uint32_t) qh[2 * j + 1] << 16);
+                const uint32_t lo  = (c & 2) ? ((lo4 >> 4) & 0x0F0F0F0Fu) : (lo4 & 0x0F0F0F0Fu);
+                const uint32_t hi  = ((hi4 >> (2 * c)) & 0x03030303u) << 4;
+                vw[j]              = lo | hi;
+            }
+            scv = (int) (int8_t) blk[192 + g];
+            d   = f16_bits_to_f(ld_u16(blk + 208));
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (m < p.M) {
+                int isum = 0;
+                if (valid) {
+                    const int4 a   = *reinterpret_cast<const int4 *>(xq + (int64_t) m * p.K + sb * 256 + g * 16);
+                    int        dot = 0;
+                    dot            = __dp4a((int) vw[0], a.x, dot);
+                    dot            = __dp4a((int) vw[1], a.y, dot);
+                    dot            = __dp4a((int) vw[2], a.z, dot);
+                    dot            = __dp4a((int) vw[3], a.w, dot);
+                    isum           = scv * (dot - 32 * xbs[m * (p.K / 16) + sb * 16 + g]);
+                }
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) {
+                    isum += __shfl_xor_sync(0xffffffffu, isum, o);
+                }
+                if (valid && g == 0) {
+                    acc[m] = __fadd_rn(acc[m], __fmul_rn(__fmul_rn(d, xd[m * nsb + sb]), (float) isum));
+                }
+            }
+        }
+    }
+}
+
+template <int QT, int MT>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // shared layout: [barriers][reduction][x quants][x scales][x bsums][stages]
+    uint64_t * full  = reinterpret_cast<uint64_t *>(smem);
+    uint64_t * empty = full + 4;
+    double *   red   = reinterpret_cast<double *>(smem + 64);
+    int8_t *   xq    = reinterpret_cast<int8_t *>(smem + 128);
+    const int  xq_bytes = (MT * p.K + 15) / 16 * 16;
+    float *    xd       = reinterpret_cast<float *>(smem + 128 + xq_bytes);
+    const int  nscale   = QT == ACB_TYPE_Q8_0 ? p.K / 32 : p.K / 256;
+    const int  xd_bytes = (MT * nscale * 4 + 15) / 16 * 16;
+    int *      xbs      = reinterpret_cast<int *>(smem + 128 + xq_bytes + xd_bytes);
+    const int  bs_bytes = QT == ACB_TYPE_Q8_0 ? 0 : (MT * (p.K / 16) * 4 + 15) / 16 * 16;
+    const int  st_off   = (128 + xq_bytes + xd_bytes + bs_bytes + 127) / 128 * 128;
+    uint8_t *  stages   = smem + st_off;
+
+    const int64_t row0   = (int64_t) blockIdx.x * p.rows_per_cta;
+    const int64_t row1   = row0 + p.rows_per_cta < p.N ? row0 + p.rows_per_cta : p.N;
+    const int     nrows  = row1 > row0 ? (int) (row1 - row0) : 0;
+    const int     nchunk = (nrows + p.chunk_rows - 1) / p.chunk_rows;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; s++) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], kConsumerWarps);
+        }
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    ptx::grid_dep_launch();
+
+    if (warp == kConsumerWarps) {
+        // producer: stream this CTA's rows (independent of the previous kernel's output)
+        if (lane == 0) {
+            const uint64_t pol = ptx::policy_evict_first();
+            for (int i = 0; i < nchunk; i++) {
+                const int s = i % p.stages;
+                if (i >= p.stages && !ptx::mbar_wait(&empty[s], ((i / p.stages) - 1) & 1)) {
+                    if (p.err) {
+                        atomicOr(p.err, ACB_DEVERR_TIMEOUT);
+                    }
+                    break;
+                }
+                const int64_t r     = row0 + (int64_t) i * p.chunk_rows;
+                const int     rows  = (int) ((row1 - r) < p.chunk_rows ? (row1 - r) : p.chunk_rows);
+                const uint32_t bytes = (uint32_t) (((int64_t) rows * p.row_bytes + 15) / 16 * 16);
+                ptx::mbar_arrive_expect_tx(&full[s], bytes);
+                ptx::bulk_g2s_stream(stages + (int64_t) s * p.stage_bytes, p.W + r * p.row_bytes, bytes, &full[s],
+                                     pol);
+            }
+        }
+        return;
+    }
+
+    // consumers: activation prologue once the previous kernel's output is visible
+    ptx::grid_dep_wait();
+    if (QT == ACB_TYPE_Q8_0) {
+        quantize_q8_0(p, xq, xd, red);
+    } else {
+        quantize_q8_K(p, xq, xd, xbs, red);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+
+    for (int i = 0; i < nchunk; i++) {
+        const int s = i % p.stages;
+        if (!ptx::mbar_wait(&full[s], (i / p.stages) & 1)) {
+            if (lane == 0 && p.err) {
+                atomicOr(p.err, ACB_DEVERR_TIMEOUT);
+            }
+            return;
+        }
+        const int64_t   r     = row0 + (int64_t) i * p.chunk_rows;
+        const int       rows  = (int) ((row1 - r) < p.chunk_rows ? (row1 - r) : p.chunk_rows);
+        const uint8_t * stage = stages + (int64_t) s * p.stage_bytes;
+        for (int rr = warp; rr < rows; rr += kConsumerWarps) {
+            float acc[MT];
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                acc[m] = 0.0f;
+            }
+            const uint8_t * wrow = stage + (int64_t) rr * p.row_bytes;
+            if (QT == ACB_TYPE_Q8_0) {
+                dot_q8_0<MT>(wrow, p, xq, xd, acc);
+            } else if (QT == ACB_TYPE_Q4_K) {
+                dot_q4_K<MT>(wrow, p, xq, xd, xbs, acc);
+            } else {
+                dot_q6_K<MT>(wrow, p, xq, xd, xbs, acc);
+            }
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                if (m < p.M) {
+                    const float v = warp_sum(acc[m]);
+                    if (lane == 0) {
+                        const int64_t n  = r + rr;
+                        float *       yp = p.y + (int64_t) m * p.y_stride + n;
+                        *yp = p.epilogue == EPI_ADD ? __fadd_rn(p.res[(int64_t) m * p.res_stride + n], v) : v;
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            ptx::mbar_arrive(&empty[s]);
+        }
+    }
+}
+
+template <int QT, int MT>
+static acb_status launch_gemv(GemvParams p, bool pdl, cudaStream_t st) {
+    const int sms = num_sms();
+    // rows must start on 16-byte boundaries for the bulk copies
+    int align = 1;
+    while ((p.row_bytes * align) % 16 != 0) {
+        align++;
+    }
+    // ~32 KB stages, 3-4 deep, leaving room for a second CTA of the next kernel (PDL)
+    int chunk = (int) (32768 / p.row_bytes);
+    chunk     = chunk < 1 ? 1 : chunk;
+    chunk     = (chunk + align - 1) / align * align;
+    int64_t per_cta = (p.N + sms - 1) / sms;
+    per_cta         = (per_cta + align - 1) / align * align;
+    if (chunk > per_cta) {
+        chunk = (int) per_cta;
+    }
+    p.rows_per_cta = (int) per_cta;
+    p.chunk_rows   = chunk;
+    p.stage_bytes  = (int) (((int64_t) chunk * p.row_bytes + 15) / 16 * 16);
+    const int nscale   = QT == ACB_TYPE_Q8_0 ? p.K / 32 : p.K / 256;
+    const int xq_bytes = (MT * p.K + 15) / 16 * 16;
+    const int xd_bytes = (MT * nscale * 4 + 15) / 16 * 16;
+    const int bs_bytes = QT == ACB_TYPE_Q8_0 ? 0 : (MT * (p.K / 16) * 4 + 15) / 16 * 16;
+    const int st_off   = (128 + xq_bytes + xd_bytes + bs_bytes + 127) / 128 * 128;
+    const int64_t chunks_per_cta = (per_cta + chunk - 1) / chunk;
+    int stages = chunks_per_cta < 4 ? (int) chunks_per_cta : 4;
+    while (stages > 1 && st_off + (int64_t) stages * p.stage_bytes > 110 * 1024) {
+        stages--;
+    }
+    p.stages = stages < 1 ? 1 : stages;
+    const int64_t smem = st_off + (int64_t) p.stages * p.stage_bytes;
+    if (smem > 220 * 1024) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const int grid = (int) ((p.N + per_cta - 1) / per_cta);
+    auto      kern = gemv_kernel<QT, MT>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) grid);
+    cfg.blockDim           = dim3(kThreads);
+    cfg.dynamicSmemBytes   = (size_t) smem;
+    cfg.stream             = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = pdl ? attr : nullptr;
+    cfg.numAttrs                                       = pdl ? 1 : 0;
+    cudaError_t e                                      = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+template <int QT>
+static acb_status dispatch_m(const GemvParams & p, bool pdl, cudaStream_t st) {
+    if (p.M <= 1) {
+        return launch_gemv<QT, 1>(p, pdl, st);
+    }
+    if (p.M <= 2) {
+        return launch_gemv<QT, 2>(p, pdl, st);
+    }
+    if (p.M <= 4) {
+        return launch_gemv<QT, 4>(p, pdl, st);
+    }
+    return launch_gemv<QT, 8>(p, pdl, st);
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" acb_status acb_gemv(const void * W, int w_type, int64_t N, int64_t K, int M, int prologue, const float * x,
+                               int64_t x_stride, const float * norm_w, float eps, int n_split, float * y,
+                               int64_t y_stride, int epilogue, const float * res, int64_t res_stride, int flags,
+                               int * err_flag, acb_stream_t stream) {
+    if (!W || !x || !y || N <= 0 || K <= 0 || M <= 0 || M > 8 || y_stride < N) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (prologue < PRO_X || prologue > PRO_SWIGLU || (prologue == PRO_SUM_SPLITS && n_split < 1)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (epilogue == EPI_ADD && !res) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(W) % 16 != 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    GemvParams p = {};
+    p.W          = (const uint8_t *) W;
+    p.N          = N;
+    p.K          = (int) K;
+    p.M          = M;
+    p.prologue   = prologue;
+    p.x          = x;
+    p.x_stride   = x_stride;
+    p.norm_w     = norm_w;
+    p.eps        = eps;
+    p.n_split    = n_split;
+    p.y          = y;
+    p.y_stride   = y_stride;
+    p.epilogue   = epilogue;
+    p.res        = res;
+    p.res_stride = res_stride;
+    p.err        = err_flag;
+    const bool   pdl = (flags & 1) != 0;
+    cudaStream_t st  = (cudaStream_t) stream;
+    switch (w_type) {
+        case ACB_TYPE_Q8_0:
+            if (K % 256 != 0) {
+                return ACB_ERR_UNSUPPORTED;
+            }
+            p.row_bytes = K / 32 * 34;
+            return dispatch_m<ACB_TYPE_Q8_0>(p, pdl, st);
+        case ACB_TYPE_Q4_K:
+            if (K % 256 != 0) {
+                return ACB_ERR_UNSUPPORTED;
+            }
+            p.row_bytes = K / 256 * 144;
+            return dispatch_m<ACB_TYPE_Q4_K>(p, pdl, st);
+        case ACB_TYPE_Q6_K:
+            if (K % 256 != 0) {
+                return ACB_ERR_UNSUPPORTED;
+            }
+            p.row_bytes = K / 256 * 210;
+            return dispatch_m<ACB_TYPE_Q6_K>(p, pdl, st);
+        default:
+            return ACB_ERR_UNSUPPORTED;
+    }
+}

@@ -130,6 +130,79 @@ ACB_API acb_status acb_get_rows(const void * table, int table_type, int64_t n_ro
                         int64_t n_ids, void * out, int out_type, int64_t out_stride, int * err_flag,
                         acb_stream_t stream);
 
+/* Quantise f32 rows [rows][K] (device) into GGUF blocks at dst (device): Q8_0 with ggml's
+ * reference quantiser arithmetic (d = amax/127 as f16, q = roundf(x/d)); Q4_K and Q6_K with
+ * min/max encoders that produce valid blocks. Used to build synthetic weights and to requantise
+ * on device (the reference requantises on the host in src/adapter-merge.h:357-472). */
+ACB_API acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int type, void * dst, acb_stream_t stream);
+
+/* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
+
+enum {
+    ACB_PRO_X          = 0, /* activation x[m][k] = x[m*x_stride + k] */
+    ACB_PRO_RMSNORM    = 1, /* x = rms_norm(h[m]) * norm_w (h = x argument) */
+    ACB_PRO_SUM_SPLITS = 2, /* x[m][k] = sum_s x[(m*n_split + s)*K + k] (attention split partials) */
+    ACB_PRO_SWIGLU     = 3, /* x[m][k] = silu(g[m][k]) * g[m][K + k], g rows of 2K at x_stride */
+};
+enum {
+    ACB_EPI_STORE = 0, /* y = W.x */
+    ACB_EPI_ADD   = 1, /* y = res + W.x (ggml_add(hidden, out); y may alias res) */
+};
+enum {
+    ACB_FLAG_PDL = 1, /* launch with programmatic dependent launch (the kernel waits on its
+                         predecessor with griddepcontrol.wait before reading activations) */
+};
+
+/* Weight-streaming GEMV for M = 1..8 rows: y[m][n] = sum_k W[n][k] * x[m][k] for W = N rows of K
+ * elements in Q8_0, Q4_K or Q6_K (K a multiple of 256; W 16-byte aligned and readable up to the
+ * next 16-byte boundary past its last row). The activation is quantised in-kernel to the
+ * weight's ggml vec-dot type (Q8_0 / Q8_K) and dotted with integer arithmetic, exactly like
+ * ggml-CPU's quantised mul_mat; `prologue` fuses the producer of x and `epilogue` the residual
+ * add. Replaces ggml_mul_mat at every decode linear (src/qwen3-lm.h:639-651, 747-755) together
+ * with the ggml_rms_norm/ggml_mul before it (qwen3-lm.h:636,741), ggml_swiglu
+ * (qwen3-enc.h:217) and ggml_add after it (qwen3-lm.h:730,738). */
+ACB_API acb_status acb_gemv(const void * W, int w_type, int64_t N, int64_t K, int M, int prologue, const float * x,
+                            int64_t x_stride, const float * norm_w, float eps, int n_split, float * y,
+                            int64_t y_stride, int epilogue, const float * res, int64_t res_stride, int flags,
+                            int * err_flag, acb_stream_t stream);
+
+/* Fused QKV post-processing for the KV-cache path, head_dim 128: for every token t and every
+ * head of the fused [q(Nh) | k(Nkv) | v(Nkv)] row (f32, token stride qkv_stride): q heads ->
+ * RMSNorm*q_norm + NeoX RoPE -> q_out (f32); k heads -> RMSNorm*k_norm + RoPE -> f16 k_cache;
+ * v heads -> f16 v_cache. Cache element (set, h, p, d) is at ((set*Nkv + h)*max_seq + p)*128 + d
+ * (the reference's 4-D [D, max_seq, Nkv, n_sets] tensor); token t uses set
+ * set0 + t*set_per_tok and position pos[t]. Replaces qw3lm_build_attn's q/k-norm, rope and
+ * ggml_cpy into the cache (src/qwen3-lm.h:366-406; batched: 654-703). */
+ACB_API acb_status acb_qkv_post(const float * qkv, int64_t qkv_stride, int64_t n_tok, int Nh, int Nkv, int head_dim,
+                                const float * q_norm, const float * k_norm, float eps, const int32_t * pos,
+                                const float * rope_table, int max_pos, float * q_out, int64_t q_stride,
+                                uint16_t * k_cache, uint16_t * v_cache, int max_seq, int set0, int set_per_tok,
+                                int flags, int * err_flag, acb_stream_t stream);
+
+/* Number of KV splits acb_attn_decode uses for n_tok sequences of Nkv heads on this device. */
+ACB_API int acb_attn_decode_splits(int n_tok, int Nkv);
+
+/* One-token attention for n_tok sequences over the f16 cache, kv_len = pos[t] + 1, with
+ * ggml-CPU semantics (q and normalised probabilities rounded to f16, softmax sum in double).
+ * Scratch (device, caller-owned): scores [n_tok][Nh][max_seq] f32, smax [n_tok][Nh][n_split]
+ * f32; output: part [n_tok][n_split][Nh*128] f32 split partials, summed by the O-projection's
+ * ACB_PRO_SUM_SPLITS prologue. Replaces ggml_flash_attn_ext / qwen3_attn_f32 on the cache view
+ * (src/qwen3-lm.h:705-723). */
+ACB_API acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok, int Nh, int Nkv, int head_dim,
+                                   const int32_t * pos, const uint16_t * k_cache, const uint16_t * v_cache,
+                                   int max_seq, int set0, int set_per_tok, float scale, int n_split, float * scores,
+                                   float * smax, float * part, int flags, acb_stream_t stream);
+
+/* Greedy sampling on device: ids[r] = argmax_v logits[r*stride + v] (lowest index on ties),
+ * margin[r] = top1 - top2 (optional), pos_advance[r] += 1 (optional: advances the next step's
+ * positions without a host round trip). With hist (requires pos_advance and hist_base) the
+ * token is also recorded at hist[r*hist_stride + pos_advance[r] - hist_base[r]] (and its margin
+ * in mhist when given) before the position advances. Replaces the temperature-0 branch of
+ * sample_top_k_p (src/sampling.h:30-34). */
+ACB_API acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids, float * margin,
+                              int32_t * pos_advance, int32_t * hist, float * mhist, int64_t hist_stride,
+                              const int32_t * hist_base, int flags, acb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

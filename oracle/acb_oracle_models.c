@@ -75,7 +75,25 @@ static int qwen3_layer(const orc_qwen3 * m, const orc_qwen3_layer * ly, float * 
     int       rc   = 0;
 
     orc_rms_norm(hidden, (const float *) ly->attn_norm.data, norm, S, H, m->eps);
-    rc |= linear(&ly->qkv, norm, S, qkv);
+    if (ly->qkv.data) {
+        rc |= linear(&ly->qkv, norm, S, qkv);
+    } else {
+        /* separate projections: same row-wise products, written into the fused layout */
+        float * t = fbuf((int64_t) S * qd);
+        rc |= linear(&ly->q, norm, S, t);
+        for (int s = 0; s < S; s++) {
+            memcpy(qkv + (int64_t) s * qkvd, t + (int64_t) s * qd, sizeof(float) * qd);
+        }
+        rc |= linear(&ly->k, norm, S, t);
+        for (int s = 0; s < S; s++) {
+            memcpy(qkv + (int64_t) s * qkvd + qd, t + (int64_t) s * kvd, sizeof(float) * kvd);
+        }
+        rc |= linear(&ly->v, norm, S, t);
+        for (int s = 0; s < S; s++) {
+            memcpy(qkv + (int64_t) s * qkvd + qd + kvd, t + (int64_t) s * kvd, sizeof(float) * kvd);
+        }
+        free(t);
+    }
     orc_qk_norm_rope(qkv, qkvd, q, qd, S, Nh, D, (const float *) ly->q_norm.data, m->eps, rope);
     orc_qk_norm_rope(qkv + qd, qkvd, k, kvd, S, Nkv, D, (const float *) ly->k_norm.data, m->eps, rope);
     for (int s = 0; s < S; s++) {
@@ -128,7 +146,20 @@ static int qwen3_layer(const orc_qwen3 * m, const orc_qwen3_layer * ly, float * 
     add_inplace(hidden, o, (int64_t) S * H);
 
     orc_rms_norm(hidden, (const float *) ly->post_norm.data, norm, S, H, m->eps);
-    rc |= linear(&ly->gate_up, norm, S, gu);
+    if (ly->gate_up.data) {
+        rc |= linear(&ly->gate_up, norm, S, gu);
+    } else {
+        float * t = fbuf((int64_t) S * F);
+        rc |= linear(&ly->gate, norm, S, t);
+        for (int s = 0; s < S; s++) {
+            memcpy(gu + (int64_t) s * 2 * F, t + (int64_t) s * F, sizeof(float) * F);
+        }
+        rc |= linear(&ly->up, norm, S, t);
+        for (int s = 0; s < S; s++) {
+            memcpy(gu + (int64_t) s * 2 * F + F, t + (int64_t) s * F, sizeof(float) * F);
+        }
+        free(t);
+    }
     orc_swiglu(gu, 2 * F, gu + F, 2 * F, act, S, F);
     rc |= linear(&ly->down, act, S, o);
     add_inplace(hidden, o, (int64_t) S * H);

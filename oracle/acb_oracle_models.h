@@ -29,13 +29,15 @@ typedef struct {
 
 typedef struct {
     orc_tensor attn_norm; /* F32 [H] */
-    orc_tensor qkv;       /* [H -> (Nh + 2 Nkv) D] */
+    orc_tensor qkv;       /* [H -> (Nh + 2 Nkv) D]; data NULL: use q, k, v below */
     orc_tensor q_norm;    /* F32 [D] */
     orc_tensor k_norm;    /* F32 [D] */
     orc_tensor o;         /* [Nh D -> H] */
     orc_tensor post_norm; /* F32 [H] */
-    orc_tensor gate_up;   /* [H -> 2 F] */
+    orc_tensor gate_up;   /* [H -> 2 F]; data NULL: use gate, up below */
     orc_tensor down;      /* [F -> H] */
+    orc_tensor q, k, v;   /* unfused projections (types differ, as gf_load_qkv_fused refuses) */
+    orc_tensor gate, up;
 } orc_qwen3_layer;
 
 typedef struct {

@@ -244,7 +244,8 @@ class Tensor(C.Structure):
 
 
 class Qwen3Layer(C.Structure):
-    _fields_ = [(n, Tensor) for n in ("attn_norm", "qkv", "q_norm", "k_norm", "o", "post_norm", "gate_up", "down")]
+    _fields_ = [(n, Tensor) for n in ("attn_norm", "qkv", "q_norm", "k_norm", "o", "post_norm", "gate_up", "down",
+                                      "q", "k", "v", "gate", "up")]
 
 
 class Qwen3(C.Structure):
@@ -310,7 +311,10 @@ class OracleQwen3:
         self.layers = (Qwen3Layer * L)()
         for i in range(L):
             for f in Qwen3Layer._fields_:
-                qt, raw, K, N = weights[f"layers.{i}.{f[0]}"]
+                key = f"layers.{i}.{f[0]}"
+                if key not in weights:  # unfused q/k/v or gate/up absent (or fused ones absent)
+                    continue
+                qt, raw, K, N = weights[key]
                 setattr(self.layers[i], f[0], tensor(raw, qt, K, N, self.keep))
         qt, raw, K, N = weights["embed"]
         emb = tensor(raw, qt, K, N, self.keep)
@@ -396,3 +400,33 @@ class OracleDiT:
                                            n_layers_run)
         assert rc == 0
         return out
+
+
+def qwen3_from_gguf_tensors(cfg, tensors):
+    """OracleQwen3 over raw GGUF tensors {name: (qtype, raw, K, N)} with the reference names
+    (model.layers.{i}.self_attn.q_proj.weight, ...), fused like gf_load_qkv_fused /
+    gf_load_pair_fused (src/gguf-weights.h:281-354) when the types match."""
+    L = cfg["num_hidden_layers"]
+    w = {"embed": tensors["model.embed_tokens.weight"], "final_norm": tensors["model.norm.weight"]}
+    for i in range(L):
+        p = f"model.layers.{i}"
+        w[f"layers.{i}.attn_norm"] = tensors[f"{p}.input_layernorm.weight"]
+        w[f"layers.{i}.post_norm"] = tensors[f"{p}.post_attention_layernorm.weight"]
+        w[f"layers.{i}.q_norm"] = tensors[f"{p}.self_attn.q_norm.weight"]
+        w[f"layers.{i}.k_norm"] = tensors[f"{p}.self_attn.k_norm.weight"]
+        w[f"layers.{i}.o"] = tensors[f"{p}.self_attn.o_proj.weight"]
+        w[f"layers.{i}.down"] = tensors[f"{p}.mlp.down_proj.weight"]
+        q, k, v = (tensors[f"{p}.self_attn.{n}_proj.weight"] for n in "qkv")
+        if q[0] == k[0] == v[0]:
+            w[f"layers.{i}.qkv"] = (q[0], np.concatenate([q[1], k[1], v[1]]), q[2], q[3] + k[3] + v[3])
+        else:
+            w[f"layers.{i}.q"], w[f"layers.{i}.k"], w[f"layers.{i}.v"] = q, k, v
+        g, u = tensors[f"{p}.mlp.gate_proj.weight"], tensors[f"{p}.mlp.up_proj.weight"]
+        if g[0] == u[0]:
+            w[f"layers.{i}.gate_up"] = (g[0], np.concatenate([g[1], u[1]]), g[2], g[3] + u[3])
+        else:
+            w[f"layers.{i}.gate"], w[f"layers.{i}.up"] = g, u
+    oc = dict(n_layers=L, H=cfg["hidden_size"], F=cfg["intermediate_size"], Nh=cfg["num_attention_heads"],
+              Nkv=cfg["num_key_value_heads"], D=cfg["head_dim"], V=cfg["vocab_size"], rope_theta=cfg["rope_theta"],
+              eps=cfg["rms_norm_eps"])
+    return OracleQwen3(oc, w)

@@ -1,0 +1,234 @@
+"""GPU parity of the decode path (configs 3 and 5) through the C ABI against the oracle.
+
+GEMV: every block contributes (float)isum * (d_w*d_x) exactly as in the oracle (activation
+quantised in-kernel to Q8_0 / Q8_K with the ggml rules, integer dot products), so the only
+difference is the order of the float sum over blocks: bar max_rel <= 2e-6 (relative to
+max |y|). Attention reproduces the f16 rounding of q and of the probabilities: bar 1e-5.
+The LM must give the same greedy tokens as the oracle's greedy loop and logits within
+cosine 0.99999 / max_rel 1e-4.
+"""
+import numpy as np
+import pytest
+
+import acb
+import oracle as O
+from helpers import assert_bitexact, cos_sim, max_rel
+from lm_fixtures import TINY, make_tensors, oracle_greedy, oracle_model, policy_all, policy_q4_k_m, write_gguf
+
+pytestmark = pytest.mark.gpu
+
+
+def T(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def TW(raw, dev):
+    """Weight rows on the device with 256 readable bytes after the last row (acb_gemv reads
+    whole 16-byte units)."""
+    import torch
+    flat = np.ascontiguousarray(raw).reshape(-1)
+    buf = torch.zeros(flat.size + 256, dtype=torch.uint8, device=dev)
+    buf[:flat.size] = torch.from_numpy(flat).to(dev)
+    return buf
+
+
+@pytest.mark.parametrize("qt", [O.Q8_0, O.Q4_K, O.Q6_K])
+@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("N,K", [(77, 256), (1000, 2048), (333, 2560), (2048, 6144)])
+def test_gemv_plain(cuda, qt, M, N, K):
+    rng = np.random.default_rng(N + K + M + qt)
+    W = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), qt)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    y = acb.gemv(TW(W, cuda), qt, N, K, T(x, cuda), M=M)
+    ref = O.mul_mat(qt, W, N, K, x)
+    assert max_rel(y.cpu().numpy(), ref) <= 2e-6
+
+
+@pytest.mark.parametrize("qt", [O.Q8_0, O.Q4_K, O.Q6_K])
+def test_gemv_rmsnorm_prologue_and_residual(cuda, qt):
+    rng = np.random.default_rng(qt)
+    M, N, K = 4, 512, 2048
+    W = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), qt)
+    h = rng.standard_normal((M, K)).astype(np.float32) * 3
+    w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    y = acb.gemv(TW(W, cuda), qt, N, K, T(h, cuda), M=M, prologue=acb.PRO_RMSNORM, norm_w=T(w, cuda),
+                 epilogue=acb.EPI_ADD, res=T(res, cuda), flags=acb.FLAG_PDL)
+    ref = res + O.mul_mat(qt, W, N, K, O.rms_norm(h, w, 1e-6))
+    assert max_rel(y.cpu().numpy() - res, ref - res) <= 2e-6
+
+
+def test_gemv_swiglu_and_split_prologues(cuda):
+    rng = np.random.default_rng(7)
+    M, N, K = 2, 256, 3072
+    W = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), O.Q8_0)
+    gu = rng.standard_normal((M, 2 * K)).astype(np.float32)
+    y = acb.gemv(TW(W, cuda), O.Q8_0, N, K, T(gu, cuda), M=M, prologue=acb.PRO_SWIGLU, x_stride=2 * K)
+    ref = O.mul_mat(O.Q8_0, W, N, K, O.swiglu(gu[:, :K], gu[:, K:]))
+    # CUDA expf can move an activation by an ulp and flip one int8 rounding: slightly looser bar
+    assert max_rel(y.cpu().numpy(), ref) <= 5e-4 and cos_sim(y.cpu().numpy(), ref) > 0.999999
+    ns = 5
+    parts = rng.standard_normal((M, ns, K)).astype(np.float32)
+    y = acb.gemv(TW(W, cuda), O.Q8_0, N, K, T(parts, cuda), M=M, prologue=acb.PRO_SUM_SPLITS, x_stride=ns * K,
+                 n_split=ns)
+    x = parts[:, 0].copy()
+    for s in range(1, ns):
+        x = (x + parts[:, s]).astype(np.float32)
+    assert max_rel(y.cpu().numpy(), O.mul_mat(O.Q8_0, W, N, K, x)) <= 2e-6
+
+
+@pytest.mark.parametrize("qt", [O.Q8_0, O.Q4_K, O.Q6_K])
+def test_device_quantize_matches_oracle_encoders(cuda, qt):
+    import torch
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((64, 2560 if qt != O.Q8_0 else 2048)) * 0.02).astype(np.float32)
+    x[3, :256] = 0.0
+    K = x.shape[1]
+    rb = acb.lib().acb_row_bytes(qt, K)
+    out = torch.empty((64, rb), dtype=torch.uint8, device=cuda)
+    acb._check("q", acb.lib().acb_quantize(T(x, cuda).data_ptr(), 64, K, qt, out.data_ptr(), acb._stream(None)))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), O.quantize(x, qt))
+
+
+@pytest.mark.parametrize("n_tok,set_per_tok", [(1, 1), (4, 1), (37, 0)])
+def test_qkv_post_and_attention(cuda, n_tok, set_per_tok):
+    import torch
+    Nh, Nkv, D, max_seq, n_sets = 16, 8, 128, 1024, 4
+    rng = np.random.default_rng(n_tok)
+    qkvd = (Nh + 2 * Nkv) * D
+    # a cache already holding random history
+    kc = (rng.standard_normal((n_sets, Nkv, max_seq, D)) * 0.5).astype(np.float16)
+    vc = rng.standard_normal((n_sets, Nkv, max_seq, D)).astype(np.float16)
+    if set_per_tok:
+        pos = rng.integers(0, max_seq, size=n_tok).astype(np.int32)
+        pos[0] = 0
+    else:
+        pos = (300 + np.arange(n_tok)).astype(np.int32)
+    qkv = rng.standard_normal((n_tok, qkvd)).astype(np.float32)
+    qn = (1 + 0.01 * rng.standard_normal(D)).astype(np.float32)
+    kn = (1 + 0.01 * rng.standard_normal(D)).astype(np.float32)
+    rope = acb.rope_table(max_seq, D, 1e6)
+    d_kc, d_vc = T(kc.view(np.uint16), cuda), T(vc.view(np.uint16), cuda)
+    q_out = torch.empty((n_tok, Nh * D), dtype=torch.float32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    d_pos = T(pos, cuda)
+    acb.qkv_post(T(qkv, cuda), n_tok, Nh, Nkv, D, T(qn, cuda), T(kn, cuda), 1e-6, d_pos, rope.to(cuda), q_out, d_kc,
+                 d_vc, max_seq, 0, set_per_tok, flags=acb.FLAG_PDL, err=err)
+    ns = acb.attn_decode_splits(n_tok, Nkv)
+    scores = torch.empty((n_tok, Nh, max_seq), dtype=torch.float32, device=cuda)
+    smax = torch.empty((n_tok, Nh, ns), dtype=torch.float32, device=cuda)
+    part = torch.empty((n_tok, ns, Nh * D), dtype=torch.float32, device=cuda)
+    acb.attn_decode(q_out, n_tok, Nh, Nkv, D, d_pos, d_kc, d_vc, max_seq, 0, set_per_tok, 1.0 / np.sqrt(D), ns,
+                    scores, smax, part, flags=acb.FLAG_PDL)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    # oracle: q/k norm + rope, cache write, attention over [0, pos]
+    rt = O.rope_cache(pos, D, 1e6)
+    qr = O.qk_norm_rope(qkv[:, :Nh * D].reshape(n_tok, Nh, D), qn, 1e-6, rt)
+    kr = O.qk_norm_rope(qkv[:, Nh * D:(Nh + Nkv) * D].reshape(n_tok, Nkv, D), kn, 1e-6, rt)
+    vr = qkv[:, (Nh + Nkv) * D:].reshape(n_tok, Nkv, D)
+    assert_bitexact(q_out.cpu().numpy().reshape(n_tok, Nh, D), qr, "q")
+    kc2, vc2 = kc.copy(), vc.copy()
+    for t in range(n_tok):
+        s = t if set_per_tok else 0
+        kc2[s, :, pos[t]] = kr[t].astype(np.float16)
+        vc2[s, :, pos[t]] = vr[t].astype(np.float16)
+    assert np.array_equal(d_kc.cpu().numpy(), kc2.view(np.uint16))
+    assert np.array_equal(d_vc.cpu().numpy(), vc2.view(np.uint16))
+    got = part.cpu().numpy().sum(axis=1)
+    for t in range(n_tok):
+        s = t if set_per_tok else 0
+        L = pos[t] + 1
+        ref = O.attention(qr[t:t + 1], kc2[s, :, :L].view(np.uint16), vc2[s, :, :L].view(np.uint16), O.F16, None,
+                          1.0 / np.sqrt(D), kv_head_major=True)
+        assert max_rel(got[t], ref.reshape(-1)) <= 1e-5, t
+
+
+def test_argmax(cuda):
+    import torch
+    rng = np.random.default_rng(5)
+    lg = rng.standard_normal((3, 217472)).astype(np.float32)
+    lg[1, 1234] = lg[1, 99] = 50.0  # tie -> lowest index
+    ids = torch.empty(3, dtype=torch.int32, device=cuda)
+    marg = torch.empty(3, dtype=torch.float32, device=cuda)
+    acb.argmax(T(lg, cuda), ids, margin=marg)
+    torch.cuda.synchronize()
+    assert ids.cpu().numpy().tolist() == [int(np.argmax(r)) for r in lg]
+    s = np.sort(lg, axis=1)
+    assert np.allclose(marg.cpu().numpy(), s[:, -1] - s[:, -2])
+
+
+# ---- whole LM ----------------------------------------------------------------------------------
+
+def _models(tmp_path, policy, seed):
+    p = str(tmp_path / "lm.gguf")
+    t = make_tensors(TINY, policy, seed=seed, embed_std=0.5)
+    write_gguf(p, TINY, t)
+    gpu = acb.QW3LM(p, max_seq_len=256, n_kv_sets=4)
+    ora = oracle_model(TINY, t)
+    ora.alloc_kv(4, 256)
+    return gpu, ora
+
+
+@pytest.mark.parametrize("policy", [policy_all(O.Q8_0), policy_q4_k_m], ids=["q8_0", "q4_k_m"])
+def test_lm_prefill_and_greedy_decode(cuda, tmp_path, policy):
+    gpu, ora = _models(tmp_path, policy, seed=21)
+    rng = np.random.default_rng(0)
+    prompt = rng.integers(0, TINY["vocab_size"], size=40).astype(np.int32)
+    lg = gpu.forward(prompt, kv_set=0)
+    lr = ora.prefill(prompt, set_=0)
+    assert cos_sim(lg, lr) > 0.99999 and max_rel(lg, lr) < 1e-4
+    assert gpu.kv_pos(0) == 40
+    # greedy: the device loop continues from the prefill's argmax
+    n = 24
+    first = int(np.argmax(lg))
+    toks, marg, _ = gpu.generate_greedy([first], 0, n, want_margins=True)
+    ora2 = oracle_model(TINY, make_tensors(TINY, policy, seed=21, embed_std=0.5))
+    ora2.alloc_kv(1, 256)
+    rtoks, rmarg = oracle_greedy(ora2, prompt, n)
+    assert toks[0].tolist() == rtoks, (toks[0].tolist(), rtoks, rmarg)
+    assert gpu.kv_pos(0) == 40 + n
+    gpu.close()
+
+
+def test_lm_forward_batch_ragged_sets(cuda, tmp_path):
+    gpu, ora = _models(tmp_path, policy_all(O.Q8_0), seed=5)
+    rng = np.random.default_rng(1)
+    lens = [7, 19, 3]
+    for s, L in enumerate(lens):
+        p = rng.integers(0, TINY["vocab_size"], size=L).astype(np.int32)
+        gpu.forward(p, kv_set=s)
+        ora.prefill(p, set_=s)
+    for step in range(3):
+        ids = rng.integers(0, TINY["vocab_size"], size=3).astype(np.int32)
+        g = gpu.forward_batch(ids, [0, 1, 2])
+        r = ora.decode(ids, set0=0)
+        for i in range(3):
+            assert cos_sim(g[i], r[i]) > 0.99999 and max_rel(g[i], r[i]) < 1e-4, (step, i)
+    # partial head: rows [lm_offset, V)
+    gpu.build_partial_head(600)
+    ids = np.array([5, 6, 7], np.int32)
+    g = gpu.forward_batch(ids, [0, 1, 2], lm_offset=600, lm_count=400)
+    r = ora.decode(ids, set0=0, lm_offset=600, lm_count=400)
+    assert g.shape == (3, 400) and max_rel(g, r) < 1e-4
+    # copy_kv then decode from the copy equals decoding the original
+    gpu.copy_kv(1, 3)
+    a = gpu.forward_batch(np.array([9], np.int32), [3])
+    b = gpu.forward_batch(np.array([9], np.int32), [1])
+    assert np.array_equal(a, b)
+    gpu.close()
+
+
+def test_lm_errors(cuda, tmp_path):
+    gpu, _ = _models(tmp_path, policy_all(O.Q8_0), seed=2)
+    with pytest.raises(acb.AcbError) as e:
+        gpu.forward(np.array([TINY["vocab_size"]], np.int32))
+    assert e.value.status == 4
+    with pytest.raises(acb.AcbError):
+        gpu.forward_batch(np.array([1, 2], np.int32), [0, 2])  # sets not consecutive
+    with pytest.raises(acb.AcbError) as e:
+        gpu.forward(np.zeros(300, np.int32))  # exceeds max_seq 256
+    assert e.value.status == 4
+    gpu.close()
