@@ -288,6 +288,16 @@ def run_ours(args):
     acb.lib()
     stream = torch.cuda.current_stream()
 
+    if args.workloads == "gemv":
+        print(json.dumps(run_gemv_shapes(dev)), flush=True)
+        return
+    if "ops" not in args.workloads.split(","):
+        # LM-only run (profiling): one line with the decode result
+        lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt, gen_len=args.lm_gen)
+        if rank == 0:
+            print(json.dumps(dict(lm, n_gpus=ws, data="synthetic", dtype="int8-dot/f32")), flush=True)
+        return
+
     table = make_q8_table(dev, 1234 + rank)
     wls = [OpsWorkload("f32", dev, table, 100 + rank), OpsWorkload("bf16", dev, table, 200 + rank)]
     ops = [(w.io, name, f, w.bytes[name]) for w in wls for name, f in w.ops()]
@@ -376,7 +386,7 @@ def run_ours(args):
     if "lm" in args.workloads.split(",") and ws == 1:
         del wls, ops, evs
         torch.cuda.empty_cache()
-        lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline)
+        lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt, gen_len=args.lm_gen)
 
     if rank == 0:
         line = {"metric": "fused-op HBM GB/s (config 2 op-chain, algorithmic bytes)", "value": round(value, 2),
@@ -404,6 +414,41 @@ def run_ours(args):
 TRAFFIC: dict = {}
 
 
+# ---- GEMV shapes of one config-3 decode step (per-launch CUDA events) -------------------------
+
+GEMV_SHAPES = [("o_proj", 2048, 2048), ("qkv", 4096, 2048), ("gate_up", 12288, 2048), ("down", 2048, 6144),
+               ("lm_head", 217472, 2048)]
+
+
+def run_gemv_shapes(dev, reps=20):
+    """Q8_0 GEMV (M=1) at every linear shape of the 1.7B decode step, each timed alone (events
+    around `reps` back-to-back launches; 3 warm-up launches first; weights > L2 only for the
+    head, so the small shapes are partly L2-served here)."""
+    import torch
+
+    import acb
+    out = {"metric": "Q8_0 GEMV GB/s per decode shape (M=1)", "shapes": {}}
+    for name, N, K in GEMV_SHAPES:
+        rb = K // 32 * 34
+        W = torch.randint(0, 256, (N * rb + 256,), dtype=torch.uint8, device=dev)
+        W[: N * rb].view(N, K // 32, 34)[:, :, 0:2] = torch.tensor([0x00, 0x14], dtype=torch.uint8, device=dev)
+        x = torch.randn(1, K, device=dev)
+        y = torch.empty(1, N, device=dev)
+        for _ in range(3):
+            acb.gemv(W, acb.Q8_0, N, K, x, y=y)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            acb.gemv(W, acb.Q8_0, N, K, x, y=y)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        nbytes = N * rb + K * 4 + N * 4
+        out["shapes"][name] = {"N": N, "K": K, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1)}
+        del W
+    return out
+
+
 # ---- workload: BASELINE config 3 (Qwen3-1.7B-shaped LM, greedy decode, batch 1) ----------------
 
 LM_PROMPT, LM_GEN = 512, 1024
@@ -418,7 +463,7 @@ def lm_weight_bytes(cfg) -> int:
     return L * per_layer + q8(V, H) + H * 4
 
 
-def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None):
+def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None, prompt_len=LM_PROMPT, gen_len=LM_GEN):
     """Config 3 on this GPU: returns the lm_decode result dict."""
     import tempfile
 
@@ -437,19 +482,21 @@ def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None):
     t_gen = time.time() - t0
     m = acb.QW3LM(path, max_seq_len=8192, n_kv_sets=1, device=dev.index or 0)
     rng = np.random.default_rng(7)
-    prompt = rng.integers(0, cfg["vocab_size"], size=LM_PROMPT).astype(np.int32)
+    prompt = rng.integers(0, cfg["vocab_size"], size=prompt_len).astype(np.int32)
     t0 = time.time()
     lg = m.forward(prompt, kv_set=0)
     t_prefill = time.time() - t0
     first = int(np.argmax(lg))
     # warm-up (captures the step graph), then the timed stretch of the 1024 generated tokens
     toks_w, _, _ = m.generate_greedy([first], 0, warm_tokens)
-    n_timed = LM_GEN - warm_tokens
+    n_timed = gen_len - warm_tokens
+    torch.cuda.profiler.start()  # profiler range = the timed decode loop (no effect without a profiler)
     toks, _, gpu_ms = m.generate_greedy([int(toks_w[0, -1])], 0, n_timed)
+    torch.cuda.profiler.stop()
     tok_s = n_timed / (gpu_ms * 1e-3)
     wb = lm_weight_bytes(cfg)
     # KV bytes read per token at the average context of the timed stretch (K and V, f16)
-    avg_ctx = LM_PROMPT + warm_tokens + n_timed / 2
+    avg_ctx = prompt_len + warm_tokens + n_timed / 2
     kv_b = int(avg_ctx * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * 2 * 2)
     per_tok_bytes = wb + kv_b
     # e2e through the reference-facing API: host ids in, host logits out, host argmax
@@ -483,7 +530,7 @@ def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None):
         "metric": "LM decode tok/s (config 3: Qwen3-1.7B shape, Q8_0, batch 1, greedy)",
         "value": round(tok_s, 2), "unit": "tok/s", "higher_is_better": True,
         "ms_per_token": round(gpu_ms / n_timed, 4),
-        "config": {"workload": "config3_lm17_q8_0_decode", "prompt": LM_PROMPT, "generated": LM_GEN,
+        "config": {"workload": "config3_lm17_q8_0_decode", "prompt": prompt_len, "generated": gen_len,
                    "timed_tokens": n_timed, "kv_cache": "f16 max_seq 8192", "weights_MB": round(wb / 1e6, 1),
                    "setup_s": {"gguf_write": round(t_gen, 1), "prefill": round(t_prefill, 2)}},
         "hbm": {"bytes_per_token": per_tok_bytes, "achieved_GBs": round(per_tok_bytes * tok_s / 1e9, 1),
@@ -539,8 +586,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
+    ap.add_argument("--lm-gen", type=int, default=LM_GEN)
     ap.add_argument("--workloads", default="ops,lm",
-                    help="comma list: ops (config 2, the headline line), lm (config 3 decode, N=1)")
+                    help="comma list: ops (config 2, the headline line), lm (config 3 decode, N=1); "
+                         "or `gemv` alone for the per-shape GEMV microbench")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

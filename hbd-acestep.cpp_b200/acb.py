@@ -70,7 +70,8 @@ def lib():
             "acb_qkv_post": (I, [P, I64, I64, I, I, I, P, P, F, P, P, I, P, I64, P, P, I, I, I, I, P, P]),
             "acb_attn_decode_splits": (I, [I, I]),
             "acb_attn_decode": (I, [P, I64, I, I, I, I, P, P, P, I, I, I, F, I, P, P, P, I, P]),
-            "acb_argmax": (I, [P, I64, I64, I, P, P, P, P, P, I64, P, I, P]),
+            "acb_argmax_scratch_bytes": (C.c_size_t, [I, I64]),
+            "acb_argmax": (I, [P, I64, I64, I, P, P, P, P, P, I64, P, P, I, P]),
             # model level (acb_models.h)
             "acb_last_error": (C.c_char_p, []),
             "acb_gguf_open": (I, [C.c_char_p, C.POINTER(C.c_void_p)]),
@@ -251,10 +252,15 @@ def attn_decode(q, n_tok, Nh, Nkv, D, pos, k_cache, v_cache, max_seq, set0, set_
         scale, n_split, _ptr(scores), _ptr(smax), _ptr(part), flags, _stream(stream)))
 
 
-def argmax(logits, ids, margin=None, pos_advance=None, flags=0, stream=None):
+def argmax(logits, ids, margin=None, pos_advance=None, scratch=None, flags=0, stream=None):
+    import torch
     rows, V = logits.shape
+    if scratch is None:
+        scratch = torch.zeros(lib().acb_argmax_scratch_bytes(rows, V), dtype=torch.uint8, device=logits.device)
     _check("acb_argmax", lib().acb_argmax(_ptr(logits), logits.stride(0), V, rows, _ptr(ids), _ptr(margin),
-                                           _ptr(pos_advance), None, None, 0, None, flags, _stream(stream)))
+                                           _ptr(pos_advance), None, None, 0, None, _ptr(scratch), flags,
+                                           _stream(stream)))
+    return scratch
 
 
 # ---- model level ----------------------------------------------------------------------------------

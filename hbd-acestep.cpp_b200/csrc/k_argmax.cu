@@ -1,0 +1,202 @@
+// k_argmax.cu -- greedy sampling on device (the temperature-0 branch of sample_top_k_p,
+// src/sampling.h:30-34): argmax over a logits row with the lowest index winning ties, plus the
+// top1 - top2 margin.
+//
+// A row (217,472 logits = 870 KB at the BASELINE vocabulary) is split over ~50 CTAs, each
+// streaming its chunk with 16-byte loads (four in flight per thread) and reducing to a
+// (best, index, second) triple. Partials go to caller-provided scratch; the CTA that finishes
+// last (ticket counter, which it resets for the next launch) merges them and writes the token,
+// so the whole sampling step is one launch and can sit inside a CUDA graph.
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace acb {
+
+struct Best {
+    float b1;
+    float b2;
+    int   i1;
+};
+
+__device__ __forceinline__ void best_push(Best & s, float v, int i) {
+    if (v > s.b1) {
+        s.b2 = s.b1;
+        s.b1 = v;
+        s.i1 = i;
+    } else if (v > s.b2) {
+        s.b2 = v;
+    }
+}
+
+__device__ __forceinline__ void best_merge(Best & s, float ob1, float ob2, int oi) {
+    if (ob1 > s.b1 || (ob1 == s.b1 && oi < s.i1)) {
+        s.b2 = fmaxf(s.b1, ob2);
+        s.b1 = ob1;
+        s.i1 = oi;
+    } else {
+        s.b2 = fmaxf(s.b2, ob1);
+    }
+}
+
+__device__ Best block_best(Best s) {
+    __shared__ float sb1[32], sb2[32];
+    __shared__ int   si1[32];
+    const int        lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        best_merge(s, __shfl_xor_sync(0xffffffffu, s.b1, o), __shfl_xor_sync(0xffffffffu, s.b2, o),
+                   __shfl_xor_sync(0xffffffffu, s.i1, o));
+    }
+    if (lane == 0) {
+        sb1[warp] = s.b1;
+        sb2[warp] = s.b2;
+        si1[warp] = s.i1;
+    }
+    __syncthreads();
+    Best r = { sb1[0], sb2[0], si1[0] };
+    for (int w = 1; w < (int) (blockDim.x >> 5); w++) {
+        best_merge(r, sb1[w], sb2[w], si1[w]);
+    }
+    return r;
+}
+
+// scratch layout: float4 part[rows][nblk] (b1, b2, i1 bits, -) then int ticket[rows]
+template <int PDL>
+__global__ void __launch_bounds__(256) argmax_kernel(const float * __restrict__ logits, int64_t stride, int64_t V,
+                                                     int64_t chunk, int32_t * __restrict__ ids,
+                                                     float * __restrict__ margin, int32_t * __restrict__ pos_advance,
+                                                     int32_t * __restrict__ hist, float * __restrict__ mhist,
+                                                     int64_t hist_stride, const int32_t * __restrict__ hist_base,
+                                                     float4 * __restrict__ part, int * __restrict__ ticket) {
+    if (PDL) {
+        ptx::grid_dep_wait();
+    }
+    ptx::grid_dep_launch();
+    const int     row  = blockIdx.y;
+    const int     nblk = gridDim.x;
+    const float * l    = logits + (int64_t) row * stride;
+    const int64_t c0   = (int64_t) blockIdx.x * chunk;
+    const int64_t c1   = c0 + chunk < V ? c0 + chunk : V;
+    Best          s    = { -INFINITY, -INFINITY, 0x7fffffff };
+    const bool    vec  = ((reinterpret_cast<uintptr_t>(l + c0) & 15) == 0) && (chunk % 4 == 0);
+    if (vec) {
+        const int64_t nv = (c1 - c0) / 4;
+        const float4 * lv = reinterpret_cast<const float4 *>(l + c0);
+        for (int64_t v0 = threadIdx.x; v0 < nv; v0 += 4 * blockDim.x) {
+            float4 t[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int64_t vi = v0 + (int64_t) u * blockDim.x;
+                t[u]             = vi < nv ? __ldg(lv + vi) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int i = (int) (c0 + 4 * (v0 + (int64_t) u * blockDim.x));
+                if (v0 + (int64_t) u * blockDim.x < nv) {
+                    best_push(s, t[u].x, i);
+                    best_push(s, t[u].y, i + 1);
+                    best_push(s, t[u].z, i + 2);
+                    best_push(s, t[u].w, i + 3);
+                }
+            }
+        }
+        for (int64_t i = c0 + nv * 4 + threadIdx.x; i < c1; i += blockDim.x) {
+            best_push(s, l[i], (int) i);
+        }
+    } else {
+        for (int64_t i = c0 + threadIdx.x; i < c1; i += blockDim.x) {
+            best_push(s, l[i], (int) i);
+        }
+    }
+    const Best b = block_best(s);
+    __shared__ bool last;
+    if (threadIdx.x == 0) {
+        part[(int64_t) row * nblk + blockIdx.x] = make_float4(b.b1, b.b2, __int_as_float(b.i1), 0.0f);
+        __threadfence();
+        const int t = atomicAdd(ticket + row, 1);
+        last        = (t == nblk - 1);
+    }
+    __syncthreads();
+    if (!last) {
+        return;
+    }
+    // last CTA of this row: merge every partial (L2 loads, bypassing L1)
+    __threadfence();
+    Best r = { -INFINITY, -INFINITY, 0x7fffffff };
+    for (int k = threadIdx.x; k < nblk; k += blockDim.x) {
+        const float4 p = __ldcg(part + (int64_t) row * nblk + k);
+        best_merge(r, p.x, p.y, __float_as_int(p.z));
+    }
+    const Best f = block_best(r);
+    if (threadIdx.x == 0) {
+        ticket[row] = 0;
+        ids[row]    = f.i1;
+        if (margin) {
+            margin[row] = f.b1 - f.b2;
+        }
+        if (pos_advance) {
+            if (hist && hist_base) {
+                const int64_t step             = pos_advance[row] - hist_base[row];
+                hist[row * hist_stride + step] = f.i1;
+                if (mhist) {
+                    mhist[row * hist_stride + step] = f.b1 - f.b2;
+                }
+            }
+            pos_advance[row] += 1;
+        }
+    }
+}
+
+static int argmax_blocks(int64_t V) {
+    int64_t n = (V + 4095) / 4096;
+    return (int) (n < 1 ? 1 : (n > 128 ? 128 : n));
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" size_t acb_argmax_scratch_bytes(int rows, int64_t V) {
+    if (rows <= 0 || V <= 0) {
+        return 0;
+    }
+    return (size_t) rows * argmax_blocks(V) * sizeof(float4) + (size_t) rows * sizeof(int) + 16;
+}
+
+extern "C" acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
+                                 float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
+                                 int64_t hist_stride, const int32_t * hist_base, void * scratch, int flags,
+                                 acb_stream_t stream) {
+    if (!logits || !ids || !scratch || V <= 0 || V > INT32_MAX || rows <= 0 || stride < V ||
+        (hist && (!pos_advance || !hist_base))) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (reinterpret_cast<uintptr_t>(scratch) % 16 != 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int     nblk   = argmax_blocks(V);
+    int64_t       chunk  = (V + nblk - 1) / nblk;
+    chunk                = (chunk + 3) / 4 * 4;
+    float4 *      part   = reinterpret_cast<float4 *>(scratch);
+    int *         ticket = reinterpret_cast<int *>(part + (size_t) rows * nblk);
+    const dim3    grid((unsigned) nblk, (unsigned) rows);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = grid;
+    cfg.blockDim           = dim3(256);
+    cfg.stream             = (cudaStream_t) stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const bool pdl                                     = flags & 1;
+    cfg.attrs                                          = pdl ? attr : nullptr;
+    cfg.numAttrs                                       = pdl ? 1 : 0;
+    cudaError_t e = pdl ? cudaLaunchKernelEx(&cfg, argmax_kernel<1>, logits, stride, V, chunk, ids, margin,
+                                             pos_advance, hist, mhist, hist_stride, hist_base, part, ticket)
+                        : cudaLaunchKernelEx(&cfg, argmax_kernel<0>, logits, stride, V, chunk, ids, margin,
+                                             pos_advance, hist, mhist, hist_stride, hist_base, part, ticket);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}

@@ -139,16 +139,22 @@ __global__ void __launch_bounds__(128) attn_scores_kernel(const float * __restri
     const int   j1     = min(kv_len, j0 + chunk);
     const int   set    = kv.set0 + t * kv.set_per_tok;
     __shared__ float wmax[4][G];
-    // q of the group's heads, rounded to f16 (the vec-dot type of the f16 cache)
-    float qv[G][4];
+    // 8 lanes per key: lane owns dims [16*sub, 16*sub+16) of key slot ks; q of the group's heads,
+    // rounded to f16 (the vec-dot type of the f16 cache)
+    const int sub = lane & 7, ks = lane >> 3;
+    float     qv[G][16];
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        const float4 v = *reinterpret_cast<const float4 *>(q + (int64_t) t * q_stride + (int64_t) (hk * G + g) * D +
-                                                           lane * 4);
-        qv[g][0]       = __half2float(__float2half_rn(v.x));
-        qv[g][1]       = __half2float(__float2half_rn(v.y));
-        qv[g][2]       = __half2float(__float2half_rn(v.z));
-        qv[g][3]       = __half2float(__float2half_rn(v.w));
+        const float4 * qp = reinterpret_cast<const float4 *>(q + (int64_t) t * q_stride + (int64_t) (hk * G + g) * D +
+                                                             16 * sub);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float4 v   = qp[i];
+            qv[g][4 * i]     = __half2float(__float2half_rn(v.x));
+            qv[g][4 * i + 1] = __half2float(__float2half_rn(v.y));
+            qv[g][4 * i + 2] = __half2float(__float2half_rn(v.z));
+            qv[g][4 * i + 3] = __half2float(__float2half_rn(v.w));
+        }
     }
     float mx[G];
 #pragma unroll
@@ -156,24 +162,55 @@ __global__ void __launch_bounds__(128) attn_scores_kernel(const float * __restri
         mx[g] = -INFINITY;
     }
     const uint16_t * kb = kv.k + kv_index(kv, Nkv, D, set, hk, 0);
-    for (int j = j0 + warp; j < j1; j += 4) {
-        const uint2    raw = *reinterpret_cast<const uint2 *>(kb + (int64_t) j * D + lane * 4);
-        const __half2  k01 = *reinterpret_cast<const __half2 *>(&raw.x);
-        const __half2  k23 = *reinterpret_cast<const __half2 *>(&raw.y);
-        const float2   f01 = __half22float2(k01), f23 = __half22float2(k23);
+    constexpr int    U  = 2;  // key groups in flight per lane
+    for (int jb = j0 + warp * 4; jb < j1; jb += 16 * U) {
+        uint4 raw[U][2];
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            float acc = __fmul_rn(f01.x, qv[g][0]);
-            acc       = __fadd_rn(acc, __fmul_rn(f01.y, qv[g][1]));
-            acc       = __fadd_rn(acc, __fmul_rn(f23.x, qv[g][2]));
-            acc       = __fadd_rn(acc, __fmul_rn(f23.y, qv[g][3]));
-            acc       = warp_sum(acc);
-            const float sv = __fmul_rn(acc, scale);
-            if (lane == 0) {
-                scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j] = sv;
+        for (int u = 0; u < U; u++) {
+            const int j = jb + 16 * u + ks;
+            if (j < j1) {
+                const uint4 * src = reinterpret_cast<const uint4 *>(kb + (int64_t) j * D + 16 * sub);
+                raw[u][0]         = src[0];
+                raw[u][1]         = src[1];
             }
-            mx[g] = fmaxf(mx[g], sv);
         }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = jb + 16 * u + ks;
+            float     kf[16];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const __half2 * hp = reinterpret_cast<const __half2 *>(&raw[u][h]);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float2 f      = __half22float2(hp[e]);
+                    kf[8 * h + 2 * e]     = f.x;
+                    kf[8 * h + 2 * e + 1] = f.y;
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    acc = __fadd_rn(acc, __fmul_rn(kf[e], qv[g][e]));
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+                const float sv = __fmul_rn(acc, scale);
+                if (j < j1) {
+                    if (sub == 0) {
+                        scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j] = sv;
+                    }
+                    mx[g] = fmaxf(mx[g], sv);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        mx[g] = warp_max(mx[g]);
     }
     if (lane == 0) {
 #pragma unroll
@@ -253,19 +290,38 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
         }
     }
     const uint16_t * vb = kv.v + kv_index(kv, Nkv, D, set, hk, 0);
-    for (int j = j0 + warp; j < j1; j += 4) {
-        const uint2   raw = *reinterpret_cast<const uint2 *>(vb + (int64_t) j * D + lane * 4);
-        const float2  f01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
-        const float2  f23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+    const float *    sb = scores + (int64_t) t * Nh * s_stride + (int64_t) (hk * G) * s_stride;
+    constexpr int    U  = 4;  // keys in flight per warp
+    for (int jb = j0 + warp; jb < j1; jb += 4 * U) {
+        uint2 raw[U];
+        float sv[U][G];
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float sv = scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j];
-            const float pe = __fmul_rn(expf(__fsub_rn(sv, sM[g])), sInv[g]);
-            const float pp = __half2float(__float2half_rn(pe));
-            acc[g][0]      = __fadd_rn(acc[g][0], __fmul_rn(f01.x, pp));
-            acc[g][1]      = __fadd_rn(acc[g][1], __fmul_rn(f01.y, pp));
-            acc[g][2]      = __fadd_rn(acc[g][2], __fmul_rn(f23.x, pp));
-            acc[g][3]      = __fadd_rn(acc[g][3], __fmul_rn(f23.y, pp));
+        for (int u = 0; u < U; u++) {
+            const int j = jb + 4 * u;
+            if (j < j1) {
+                raw[u] = *reinterpret_cast<const uint2 *>(vb + (int64_t) j * D + lane * 4);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    sv[u][g] = sb[(int64_t) g * s_stride + j];
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = jb + 4 * u;
+            if (j < j1) {
+                const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].x));
+                const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].y));
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const float pe = __fmul_rn(expf(__fsub_rn(sv[u][g], sM[g])), sInv[g]);
+                    const float pp = __half2float(__float2half_rn(pe));
+                    acc[g][0]      = __fadd_rn(acc[g][0], __fmul_rn(f01.x, pp));
+                    acc[g][1]      = __fadd_rn(acc[g][1], __fmul_rn(f01.y, pp));
+                    acc[g][2]      = __fadd_rn(acc[g][2], __fmul_rn(f23.x, pp));
+                    acc[g][3]      = __fadd_rn(acc[g][3], __fmul_rn(f23.y, pp));
+                }
+            }
         }
     }
     // reduce the 4 warps through shared memory, then write the split partial [t][split][Nh*D]
@@ -289,81 +345,6 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
         float4 * dst = reinterpret_cast<float4 *>(part + ((int64_t) t * n_split + split) * Nh * D +
                                                   (int64_t) (hk * G + g) * D + lane * 4);
         *dst         = r;
-    }
-}
-
-// ---- greedy argmax over logits rows; optionally advances positions for the next step --------
-template <int PDL>
-__global__ void __launch_bounds__(1024) argmax_kernel(const float * __restrict__ logits, int64_t stride, int64_t V,
-                                                      int32_t * __restrict__ ids, float * __restrict__ margin,
-                                                      int32_t * __restrict__ pos_advance,
-                                                      int32_t * __restrict__ hist, float * __restrict__ mhist,
-                                                      int64_t hist_stride, const int32_t * __restrict__ hist_base) {
-    dep_wait<PDL>();
-    ptx::grid_dep_launch();
-    const int     row = blockIdx.x;
-    const float * l   = logits + (int64_t) row * stride;
-    float         b1 = -INFINITY, b2 = -INFINITY;
-    int           i1 = 0x7fffffff;
-    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = l[i];
-        if (v > b1) {
-            b2 = b1;
-            b1 = v;
-            i1 = (int) i;
-        } else if (v > b2) {
-            b2 = v;
-        }
-    }
-    __shared__ float sb1[32], sb2[32];
-    __shared__ int   si1[32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ob1 = __shfl_xor_sync(0xffffffffu, b1, o);
-        const float ob2 = __shfl_xor_sync(0xffffffffu, b2, o);
-        const int   oi  = __shfl_xor_sync(0xffffffffu, i1, o);
-        if (ob1 > b1 || (ob1 == b1 && oi < i1)) {
-            b2 = fmaxf(b1, ob2);
-            b1 = ob1;
-            i1 = oi;
-        } else {
-            b2 = fmaxf(b2, ob1);
-        }
-    }
-    if (lane == 0) {
-        sb1[warp] = b1;
-        sb2[warp] = b2;
-        si1[warp] = i1;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int nw = blockDim.x >> 5;
-        float     B1 = sb1[0], B2 = sb2[0];
-        int       I1 = si1[0];
-        for (int w = 1; w < nw; w++) {
-            if (sb1[w] > B1 || (sb1[w] == B1 && si1[w] < I1)) {
-                B2 = fmaxf(B1, sb2[w]);
-                B1 = sb1[w];
-                I1 = si1[w];
-            } else {
-                B2 = fmaxf(B2, sb1[w]);
-            }
-        }
-        ids[row] = I1;
-        if (margin) {
-            margin[row] = B1 - B2;
-        }
-        if (pos_advance) {
-            if (hist && hist_base) {
-                const int64_t step = pos_advance[row] - hist_base[row];
-                hist[row * hist_stride + step] = I1;
-                if (mhist) {
-                    mhist[row * hist_stride + step] = B1 - B2;
-                }
-            }
-            pos_advance[row] += 1;
-        }
     }
 }
 
@@ -461,19 +442,4 @@ extern "C" acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_t
     ACB_ATT(8)
 #undef ACB_ATT
     return ACB_ERR_UNSUPPORTED;
-}
-
-extern "C" acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
-                                 float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
-                                 int64_t hist_stride, const int32_t * hist_base, int flags, acb_stream_t stream) {
-    if (!logits || !ids || V <= 0 || rows <= 0 || stride < V || (hist && (!pos_advance || !hist_base))) {
-        return ACB_ERR_INVALID_ARG;
-    }
-    const bool pdl = flags & 1;
-    if (pdl) {
-        return launch_ex(argmax_kernel<1>, dim3((unsigned) rows), dim3(1024), 0, (cudaStream_t) stream, true, logits,
-                         stride, V, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base);
-    }
-    return launch_ex(argmax_kernel<0>, dim3((unsigned) rows), dim3(1024), 0, (cudaStream_t) stream, false, logits,
-                     stride, V, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base);
 }

@@ -50,38 +50,61 @@ struct GemvParams {
 };
 
 // ---- activation value of element k of row m under the prologue ------------------------------
-__device__ __forceinline__ float act_value(const GemvParams & p, int m, int k, float sc) {
-    switch (p.prologue) {
-        case PRO_RMSNORM: {
-            const float h = p.x[(int64_t) m * p.x_stride + k];
-            const float v = __fmul_rn(h, sc);
-            return p.norm_w ? __fmul_rn(v, __ldg(p.norm_w + k)) : v;
+// (raw loads first, `act_finish` after, so a round of loads is in flight at once)
+template <int PRO> struct ActRaw {
+    float a, b;
+};
+
+template <int PRO> __device__ __forceinline__ ActRaw<PRO> act_load(const GemvParams & p, int m, int k) {
+    ActRaw<PRO>   r{ 0.0f, 0.0f };
+    const float * row = p.x + (int64_t) m * p.x_stride;
+    if (PRO == PRO_SUM_SPLITS) {
+        float s = row[k];
+        for (int i = 1; i < p.n_split; i++) {
+            s = __fadd_rn(s, row[(int64_t) i * p.K + k]);
         }
-        case PRO_SUM_SPLITS: {
-            const float * b = p.x + (int64_t) m * p.x_stride + k;
-            float         s = b[0];
-            for (int i = 1; i < p.n_split; i++) {
-                s = __fadd_rn(s, b[(int64_t) i * p.K]);
-            }
-            return s;
-        }
-        case PRO_SWIGLU: {
-            const float g = p.x[(int64_t) m * p.x_stride + k];
-            const float u = p.x[(int64_t) m * p.x_stride + p.K + k];
-            return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-        }
-        default:
-            return p.x[(int64_t) m * p.x_stride + k];
+        r.a = s;
+    } else if (PRO == PRO_SWIGLU) {
+        r.a = row[k];
+        r.b = row[p.K + k];
+    } else if (PRO == PRO_RMSNORM) {
+        r.a = row[k];
+        r.b = p.norm_w ? __ldg(p.norm_w + k) : 1.0f;
+    } else {
+        r.a = row[k];
     }
+    return r;
+}
+
+template <int PRO> __device__ __forceinline__ float act_finish(const GemvParams & p, ActRaw<PRO> r, float sc) {
+    if (PRO == PRO_RMSNORM) {
+        const float v = __fmul_rn(r.a, sc);
+        return p.norm_w ? __fmul_rn(v, r.b) : v;
+    }
+    if (PRO == PRO_SWIGLU) {
+        return __fmul_rn(__fdiv_rn(r.a, __fadd_rn(1.0f, expf(-r.a))), r.b);
+    }
+    return r.a;
 }
 
 // RMSNorm scale of activation row m (PRO_RMSNORM), computed by the 256 consumer threads.
 __device__ float rms_scale_block(const GemvParams & p, int m, double * red) {
     const int tid = threadIdx.x;
     double    ss  = 0.0;
-    for (int k = tid; k < p.K; k += kConsumerWarps * 32) {
-        const float h = p.x[(int64_t) m * p.x_stride + k];
-        ss += (double) __fmul_rn(h, h);
+    const float * row = p.x + (int64_t) m * p.x_stride;
+    if ((p.K & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+        for (int k = tid * 4; k < p.K; k += kConsumerWarps * 32 * 4) {
+            const float4 h = *reinterpret_cast<const float4 *>(row + k);
+            ss += (double) __fmul_rn(h.x, h.x);
+            ss += (double) __fmul_rn(h.y, h.y);
+            ss += (double) __fmul_rn(h.z, h.z);
+            ss += (double) __fmul_rn(h.w, h.w);
+        }
+    } else {
+        for (int k = tid; k < p.K; k += kConsumerWarps * 32) {
+            const float h = row[k];
+            ss += (double) __fmul_rn(h, h);
+        }
     }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) {
@@ -97,38 +120,61 @@ __device__ float rms_scale_block(const GemvParams & p, int m, double * red) {
 }
 
 // ---- activation quantisers (into shared memory) ----------------------------------------------
-// Q8_0: qs int8 [M][K], d (f16-rounded, as float) [M][K/32]
+// Q8_0: qs int8 [M][K], d (f16-rounded, as float) [M][K/32]. Each warp quantises blocks
+// warp, warp+8, ... in rounds of R blocks whose loads are all issued before any reduction.
+template <int PRO>
 __device__ void quantize_q8_0(const GemvParams & p, int8_t * xq, float * xd, double * red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nb   = p.K / 32;
+    constexpr int R    = 8;
+    const int     lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int     nb   = p.K / 32;
     for (int m = 0; m < p.M; m++) {
-        const float sc = p.prologue == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
-        for (int b = warp; b < nb; b += kConsumerWarps) {
-            const float v    = act_value(p, m, b * 32 + lane, sc);
-            const float amax = warp_max(fabsf(v));
-            const float d    = amax / 127.0f;
-            const float id   = d != 0.0f ? 1.0f / d : 0.0f;
-            xq[(int64_t) m * p.K + b * 32 + lane] = (int8_t) roundf(__fmul_rn(v, id));
-            if (lane == 0) {
-                xd[m * nb + b] = __half2float(__float2half_rn(d));
+        const float sc = PRO == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
+        for (int b0 = warp; b0 < nb; b0 += kConsumerWarps * R) {
+            ActRaw<PRO> raw[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int b = b0 + r * kConsumerWarps;
+                if (b < nb) {
+                    raw[r] = act_load<PRO>(p, m, b * 32 + lane);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int b = b0 + r * kConsumerWarps;
+                if (b < nb) {
+                    const float v    = act_finish<PRO>(p, raw[r], sc);
+                    const float amax = warp_max(fabsf(v));
+                    const float d    = amax / 127.0f;
+                    const float id   = d != 0.0f ? 1.0f / d : 0.0f;
+                    xq[(int64_t) m * p.K + b * 32 + lane] = (int8_t) roundf(__fmul_rn(v, id));
+                    if (lane == 0) {
+                        xd[m * nb + b] = __half2float(__float2half_rn(d));
+                    }
+                }
             }
         }
     }
 }
 
 // Q8_K: qs int8 [M][K], d float [M][K/256], bsums int [M][K/16]
+template <int PRO>
 __device__ void quantize_q8_K(const GemvParams & p, int8_t * xq, float * xd, int * xbs, double * red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nsb  = p.K / 256;
     for (int m = 0; m < p.M; m++) {
-        const float sc = p.prologue == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
+        const float sc = PRO == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
         for (int sb = warp; sb < nsb; sb += kConsumerWarps) {
             float v[8];
             float amax = 0.0f, mx = 0.0f;
             int   idx  = 0x7fffffff;
+            ActRaw<PRO> raw[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                v[j]         = act_value(p, m, sb * 256 + lane * 8 + j, sc);
+                raw[j] = act_load<PRO>(p, m, sb * 256 + lane * 8 + j);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                v[j]         = act_finish<PRO>(p, raw[j], sc);
                 const float a = fabsf(v[j]);
                 if (a > amax) {  // first index of the largest magnitude wins
                     amax = a;
@@ -353,7 +399,7 @@ __device__ __forceinline__ void dot_q6_K(const uint8_t * wrow, const GemvParams 
     }
 }
 
-template <int QT, int MT>
+template <int QT, int MT, int PRO>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -413,9 +459,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
     // consumers: activation prologue once the previous kernel's output is visible
     ptx::grid_dep_wait();
     if (QT == ACB_TYPE_Q8_0) {
-        quantize_q8_0(p, xq, xd, red);
+        quantize_q8_0<PRO>(p, xq, xd, red);
     } else {
-        quantize_q8_K(p, xq, xd, xbs, red);
+        quantize_q8_K<PRO>(p, xq, xd, xbs, red);
     }
     asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
 
@@ -463,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
     }
 }
 
-template <int QT, int MT>
+template <int QT, int MT, int PRO>
 static acb_status launch_gemv(GemvParams p, bool pdl, cudaStream_t st) {
     const int sms = num_sms();
     // rows must start on 16-byte boundaries for the bulk copies
@@ -499,7 +545,7 @@ static acb_status launch_gemv(GemvParams p, bool pdl, cudaStream_t st) {
         return ACB_ERR_UNSUPPORTED;
     }
     const int grid = (int) ((p.N + per_cta - 1) / per_cta);
-    auto      kern = gemv_kernel<QT, MT>;
+    auto      kern = gemv_kernel<QT, MT, PRO>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
 
     cudaLaunchConfig_t cfg = {};
@@ -520,18 +566,32 @@ static acb_status launch_gemv(GemvParams p, bool pdl, cudaStream_t st) {
     return ACB_OK;
 }
 
-template <int QT>
-static acb_status dispatch_m(const GemvParams & p, bool pdl, cudaStream_t st) {
+template <int QT, int PRO>
+static acb_status dispatch_mp(const GemvParams & p, bool pdl, cudaStream_t st) {
     if (p.M <= 1) {
-        return launch_gemv<QT, 1>(p, pdl, st);
+        return launch_gemv<QT, 1, PRO>(p, pdl, st);
     }
     if (p.M <= 2) {
-        return launch_gemv<QT, 2>(p, pdl, st);
+        return launch_gemv<QT, 2, PRO>(p, pdl, st);
     }
     if (p.M <= 4) {
-        return launch_gemv<QT, 4>(p, pdl, st);
+        return launch_gemv<QT, 4, PRO>(p, pdl, st);
     }
-    return launch_gemv<QT, 8>(p, pdl, st);
+    return launch_gemv<QT, 8, PRO>(p, pdl, st);
+}
+
+template <int QT>
+static acb_status dispatch_m(const GemvParams & p, bool pdl, cudaStream_t st) {
+    switch (p.prologue) {
+        case PRO_RMSNORM:
+            return dispatch_mp<QT, PRO_RMSNORM>(p, pdl, st);
+        case PRO_SUM_SPLITS:
+            return dispatch_mp<QT, PRO_SUM_SPLITS>(p, pdl, st);
+        case PRO_SWIGLU:
+            return dispatch_mp<QT, PRO_SWIGLU>(p, pdl, st);
+        default:
+            return dispatch_mp<QT, PRO_X>(p, pdl, st);
+    }
 }
 
 }  // namespace acb

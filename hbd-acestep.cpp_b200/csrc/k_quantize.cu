@@ -15,23 +15,22 @@ __device__ __forceinline__ void st_u16(uint8_t * p, uint16_t v) {
     p[1] = (uint8_t) (v >> 8);
 }
 
+// one warp per 32-element block: lane j owns element j
 __global__ void quant_q8_0_kernel(const float * __restrict__ x, int64_t nblk, uint8_t * __restrict__ dst) {
-    const int64_t b = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t b    = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int     lane = threadIdx.x & 31;
     if (b >= nblk) {
         return;
     }
-    const float * xb   = x + b * 32;
-    float         amax = 0.0f;
-    for (int j = 0; j < 32; j++) {
-        amax = fmaxf(amax, fabsf(xb[j]));
+    const float v    = x[b * 32 + lane];
+    const float amax = warp_max(fabsf(v));
+    const float d    = amax / 127.0f;
+    const float id   = d != 0.0f ? 1.0f / d : 0.0f;
+    uint8_t *   o    = dst + b * 34;  // 2-byte aligned
+    if (lane == 0) {
+        *reinterpret_cast<uint16_t *>(o) = __half_as_ushort(__float2half_rn(d));
     }
-    const float d  = amax / 127.0f;
-    const float id = d != 0.0f ? 1.0f / d : 0.0f;
-    uint8_t *   o  = dst + b * 34;
-    st_u16(o, __half_as_ushort(__float2half_rn(d)));
-    for (int j = 0; j < 32; j++) {
-        o[2 + j] = (uint8_t) (int8_t) roundf(__fmul_rn(xb[j], id));
-    }
+    o[2 + lane] = (uint8_t) (int8_t) roundf(__fmul_rn(v, id));
 }
 
 __global__ void quant_q4_K_kernel(const float * __restrict__ x, int64_t nblk, uint8_t * __restrict__ dst) {
@@ -166,7 +165,7 @@ extern "C" acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int
     const dim3   grid((unsigned) ((nblk + 127) / 128));
     cudaStream_t st = (cudaStream_t) stream;
     if (type == ACB_TYPE_Q8_0) {
-        quant_q8_0_kernel<<<grid, 128, 0, st>>>(x, nblk, (uint8_t *) dst);
+        quant_q8_0_kernel<<<dim3((unsigned) ((nblk + 7) / 8)), 256, 0, st>>>(x, nblk, (uint8_t *) dst);
     } else if (type == ACB_TYPE_Q4_K) {
         quant_q4_K_kernel<<<grid, 128, 0, st>>>(x, nblk, (uint8_t *) dst);
     } else {

@@ -96,7 +96,7 @@ struct acb_qw3lm {
     size_t               layer_elems = 0;
     int                  cap_tok     = 0;
     int                  max_split   = 1;
-    DevBuf hidden, qkv, q, scores, smax, part, gu, logits, ids, pos, err, hist_base, hist, mhist;
+    DevBuf hidden, qkv, q, scores, smax, part, gu, logits, ids, pos, err, hist_base, hist, mhist, amax;
     int32_t *                           h_ids = nullptr;
     int32_t *                           h_pos = nullptr;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -238,7 +238,7 @@ acb_status enqueue_step(acb_qw3lm * m, int N, int set0, const DevTensor * head, 
     if (greedy) {
         ACB_TRY(acb_argmax(m->logits.as<float>(), out_v, out_v, N, m->ids.as<int32_t>(), nullptr, m->pos.as<int32_t>(),
                            m->hist.as<int32_t>(), m->mhist.as<float>(), m->c.max_seq_len, m->hist_base.as<int32_t>(),
-                           ACB_FLAG_PDL, (acb_stream_t) m->st));
+                           m->amax.p, ACB_FLAG_PDL, (acb_stream_t) m->st));
     }
     return ACB_OK;
 }
@@ -419,6 +419,7 @@ extern "C" acb_status acb_qw3lm_load(const char * gguf_path, int max_seq_len, in
     f |= m->hist_base.alloc(kMaxSets * 4) != ACB_OK;
     f |= m->hist.alloc((size_t) kMaxSets * S * 4) != ACB_OK;
     f |= m->mhist.alloc((size_t) kMaxSets * S * 4) != ACB_OK;
+    f |= m->amax.alloc(acb_argmax_scratch_bytes(kMaxSets, c.vocab_size)) != ACB_OK;  // zeroed
     f |= cudaMallocHost(&m->h_ids, T * 4) != cudaSuccess;
     f |= cudaMallocHost(&m->h_pos, T * 4) != cudaSuccess;
     if (f) {

@@ -193,15 +193,21 @@ ACB_API acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok,
                                    int max_seq, int set0, int set_per_tok, float scale, int n_split, float * scores,
                                    float * smax, float * part, int flags, acb_stream_t stream);
 
+/* Device scratch (bytes) acb_argmax needs for `rows` rows of V logits. */
+ACB_API size_t acb_argmax_scratch_bytes(int rows, int64_t V);
+
 /* Greedy sampling on device: ids[r] = argmax_v logits[r*stride + v] (lowest index on ties),
  * margin[r] = top1 - top2 (optional), pos_advance[r] += 1 (optional: advances the next step's
  * positions without a host round trip). With hist (requires pos_advance and hist_base) the
  * token is also recorded at hist[r*hist_stride + pos_advance[r] - hist_base[r]] (and its margin
- * in mhist when given) before the position advances. Replaces the temperature-0 branch of
- * sample_top_k_p (src/sampling.h:30-34). */
+ * in mhist when given) before the position advances. `scratch` is a 16-byte aligned device
+ * buffer of acb_argmax_scratch_bytes(rows, V) bytes, zeroed before its first use and left
+ * reusable by every call (its counters return to zero); calls that share a scratch buffer must
+ * not overlap on the GPU. Replaces the temperature-0 branch of sample_top_k_p
+ * (src/sampling.h:30-34). */
 ACB_API acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids, float * margin,
                               int32_t * pos_advance, int32_t * hist, float * mhist, int64_t hist_stride,
-                              const int32_t * hist_base, int flags, acb_stream_t stream);
+                              const int32_t * hist_base, void * scratch, int flags, acb_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -143,7 +143,10 @@ def test_qkv_post_and_attention(cuda, n_tok, set_per_tok):
         L = pos[t] + 1
         ref = O.attention(qr[t:t + 1], kc2[s, :, :L].view(np.uint16), vc2[s, :, :L].view(np.uint16), O.F16, None,
                           1.0 / np.sqrt(D), kv_head_major=True)
-        assert max_rel(got[t], ref.reshape(-1)) <= 1e-5, t
+        # CUDA expf vs the host's can move one f16-rounded probability by an ulp (2^-11):
+        # relative effect ~5e-4 / sqrt(L) per flip
+        r, c = max_rel(got[t], ref.reshape(-1)), cos_sim(got[t], ref.reshape(-1))
+        assert r <= 1e-3 and c > 0.999999, (t, L, r, c)
 
 
 def test_argmax(cuda):
@@ -153,11 +156,21 @@ def test_argmax(cuda):
     lg[1, 1234] = lg[1, 99] = 50.0  # tie -> lowest index
     ids = torch.empty(3, dtype=torch.int32, device=cuda)
     marg = torch.empty(3, dtype=torch.float32, device=cuda)
-    acb.argmax(T(lg, cuda), ids, margin=marg)
+    scratch = acb.argmax(T(lg, cuda), ids, margin=marg)
     torch.cuda.synchronize()
     assert ids.cpu().numpy().tolist() == [int(np.argmax(r)) for r in lg]
     s = np.sort(lg, axis=1)
     assert np.allclose(marg.cpu().numpy(), s[:, -1] - s[:, -2])
+    # the scratch (ticket counters) is reusable: a second call on new data with the same scratch
+    lg2 = rng.standard_normal((3, 217472)).astype(np.float32)
+    acb.argmax(T(lg2, cuda), ids, scratch=scratch)
+    torch.cuda.synchronize()
+    assert ids.cpu().numpy().tolist() == [int(np.argmax(r)) for r in lg2]
+    # odd length (scalar tail path)
+    lg3 = rng.standard_normal((1, 1001)).astype(np.float32)
+    acb.argmax(T(lg3, cuda), ids[:1])
+    torch.cuda.synchronize()
+    assert int(ids[0].item()) == int(np.argmax(lg3))
 
 
 # ---- whole LM ----------------------------------------------------------------------------------
@@ -179,7 +192,7 @@ def test_lm_prefill_and_greedy_decode(cuda, tmp_path, policy):
     prompt = rng.integers(0, TINY["vocab_size"], size=40).astype(np.int32)
     lg = gpu.forward(prompt, kv_set=0)
     lr = ora.prefill(prompt, set_=0)
-    assert cos_sim(lg, lr) > 0.99999 and max_rel(lg, lr) < 1e-4
+    assert cos_sim(lg, lr) > 0.99999 and max_rel(lg, lr) < 1e-3, (cos_sim(lg, lr), max_rel(lg, lr))
     assert gpu.kv_pos(0) == 40
     # greedy: the device loop continues from the prefill's argmax
     n = 24
@@ -206,13 +219,14 @@ def test_lm_forward_batch_ragged_sets(cuda, tmp_path):
         g = gpu.forward_batch(ids, [0, 1, 2])
         r = ora.decode(ids, set0=0)
         for i in range(3):
-            assert cos_sim(g[i], r[i]) > 0.99999 and max_rel(g[i], r[i]) < 1e-4, (step, i)
+            assert cos_sim(g[i], r[i]) > 0.99999 and max_rel(g[i], r[i]) < 1e-3, \
+                (step, i, cos_sim(g[i], r[i]), max_rel(g[i], r[i]))
     # partial head: rows [lm_offset, V)
     gpu.build_partial_head(600)
     ids = np.array([5, 6, 7], np.int32)
     g = gpu.forward_batch(ids, [0, 1, 2], lm_offset=600, lm_count=400)
     r = ora.decode(ids, set0=0, lm_offset=600, lm_count=400)
-    assert g.shape == (3, 400) and max_rel(g, r) < 1e-4
+    assert g.shape == (3, 400) and max_rel(g, r) < 1e-3, max_rel(g, r)
     # copy_kv then decode from the copy equals decoding the original
     gpu.copy_kv(1, 3)
     a = gpu.forward_batch(np.array([9], np.int32), [3])
