@@ -69,7 +69,7 @@ def lib():
             "acb_gemv": (I, [P, I, I64, I64, I, I, P, I64, P, F, I, P, I64, I, P, I64, I, P, P]),
             "acb_qkv_post": (I, [P, I64, I64, I, I, I, P, P, F, P, P, I, P, I64, P, P, I, I, I, I, P, P]),
             "acb_attn_decode_splits": (I, [I, I]),
-            "acb_attn_decode": (I, [P, I64, I, I, I, I, P, P, P, I, I, I, F, I, P, P, P, I, P]),
+            "acb_attn_decode": (I, [P, I64, I, I, I, I, P, P, P, I, I, I, F, I, P, P, P, P, I64, P, I, P]),
             "acb_argmax_scratch_bytes": (C.c_size_t, [I, I64]),
             "acb_argmax": (I, [P, I64, I64, I, P, P, P, P, P, I64, P, P, I, P]),
             # model level (acb_models.h)
@@ -246,10 +246,11 @@ def attn_decode_splits(n_tok, Nkv):
 
 
 def attn_decode(q, n_tok, Nh, Nkv, D, pos, k_cache, v_cache, max_seq, set0, set_per_tok, scale, n_split, scores,
-                smax, part, flags=0, stream=None):
+                smax, part, out=None, tickets=None, flags=0, stream=None):
     _check("acb_attn_decode", lib().acb_attn_decode(
         _ptr(q), q.stride(0), n_tok, Nh, Nkv, D, _ptr(pos), _ptr(k_cache), _ptr(v_cache), max_seq, set0, set_per_tok,
-        scale, n_split, _ptr(scores), _ptr(smax), _ptr(part), flags, _stream(stream)))
+        scale, n_split, _ptr(scores), _ptr(smax), _ptr(part), _ptr(out), out.stride(0) if out is not None else 0,
+        _ptr(tickets), flags, _stream(stream)))
 
 
 def argmax(logits, ids, margin=None, pos_advance=None, scratch=None, flags=0, stream=None):

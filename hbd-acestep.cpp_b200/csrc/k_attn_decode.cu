@@ -8,9 +8,9 @@
 //   o   = sum_j p_j v_j                           f32 accumulation
 // The normalised probabilities are rounded before the PV product, so the step runs in two
 // passes over split chunks of the cache: pass 1 writes scores and per-split maxima, pass 2
-// normalises and forms per-split partial outputs; the O-projection GEMV sums the partials in
-// its prologue. Every CTA of a head computes the same global sum in the same order, so all
-// splits use identical normalisers.
+// normalises and forms per-split partial outputs, and the last split CTA of each head sums the
+// partials in split order. Every CTA of a head computes the same global sum in the same order,
+// so all splits use identical normalisers.
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -231,7 +231,8 @@ template <int G, int PDL>
 __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__ scores, int64_t s_stride,
                                                       const float * __restrict__ smax, int Nh, int Nkv,
                                                       const int32_t * __restrict__ pos, KvLayout kv, int n_split,
-                                                      float * __restrict__ part) {
+                                                      float * __restrict__ part, float * __restrict__ out,
+                                                      int64_t out_stride, int * __restrict__ tickets) {
     constexpr int D = 128;
     dep_wait<PDL>();
     ptx::grid_dep_launch();
@@ -345,6 +346,39 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
         float4 * dst = reinterpret_cast<float4 *>(part + ((int64_t) t * n_split + split) * Nh * D +
                                                   (int64_t) (hk * G + g) * D + lane * 4);
         *dst         = r;
+        __threadfence();
+    }
+    if (!out) {
+        return;
+    }
+    // the last split CTA of this (token, kv head) sums the partials in split order
+    __shared__ bool last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int tk = atomicAdd(tickets + t * Nkv + hk, 1);
+        last         = (tk == n_split - 1);
+    }
+    __syncthreads();
+    if (!last) {
+        return;
+    }
+    __threadfence();
+    for (int idx = threadIdx.x; idx < G * 32; idx += blockDim.x) {
+        const int     g   = idx >> 5, l = idx & 31;
+        const int64_t off = (int64_t) (hk * G + g) * D + l * 4;
+        float4        a   = __ldcg(reinterpret_cast<const float4 *>(part + (int64_t) t * n_split * Nh * D + off));
+        for (int s = 1; s < n_split; s++) {
+            const float4 b =
+                __ldcg(reinterpret_cast<const float4 *>(part + ((int64_t) t * n_split + s) * Nh * D + off));
+            a.x = __fadd_rn(a.x, b.x);
+            a.y = __fadd_rn(a.y, b.y);
+            a.z = __fadd_rn(a.z, b.z);
+            a.w = __fadd_rn(a.w, b.w);
+        }
+        *reinterpret_cast<float4 *>(out + (int64_t) t * out_stride + off) = a;
+    }
+    if (threadIdx.x == 0) {
+        tickets[t * Nkv + hk] = 0;
     }
 }
 
@@ -408,9 +442,10 @@ extern "C" int acb_attn_decode_splits(int n_tok, int Nkv) {
 extern "C" acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok, int Nh, int Nkv, int head_dim,
                                       const int32_t * pos, const uint16_t * k_cache, const uint16_t * v_cache,
                                       int max_seq, int set0, int set_per_tok, float scale, int n_split,
-                                      float * scores, float * smax, float * part, int flags, acb_stream_t stream) {
+                                      float * scores, float * smax, float * part, float * out, int64_t out_stride,
+                                      int * tickets, int flags, acb_stream_t stream) {
     if (!q || !pos || !k_cache || !v_cache || !scores || !smax || !part || n_tok <= 0 || Nh <= 0 || Nkv <= 0 ||
-        n_split < 1 || max_seq <= 0) {
+        n_split < 1 || max_seq <= 0 || (out && !tickets)) {
         return ACB_ERR_INVALID_ARG;
     }
     if (head_dim != 128 || Nh % Nkv != 0 || Nh / Nkv > 8) {
@@ -432,9 +467,11 @@ extern "C" acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_t
             return rc;                                                                                             \
         }                                                                                                          \
         return pdl ? launch_ex(attn_pv_kernel<GG, 1>, grid, dim3(128), 0, st, true, (const float *) scores,        \
-                               (int64_t) max_seq, (const float *) smax, Nh, Nkv, pos, kv, n_split, part)           \
+                               (int64_t) max_seq, (const float *) smax, Nh, Nkv, pos, kv, n_split, part, out, \
+                               out_stride, tickets)                                                                \
                    : launch_ex(attn_pv_kernel<GG, 0>, grid, dim3(128), 0, st, false, (const float *) scores,       \
-                               (int64_t) max_seq, (const float *) smax, Nh, Nkv, pos, kv, n_split, part);          \
+                               (int64_t) max_seq, (const float *) smax, Nh, Nkv, pos, kv, n_split, part, out, \
+                               out_stride, tickets);                                                               \
     }
     ACB_ATT(1)
     ACB_ATT(2)

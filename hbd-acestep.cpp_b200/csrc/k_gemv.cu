@@ -120,70 +120,136 @@ __device__ float rms_scale_block(const GemvParams & p, int m, double * red) {
 }
 
 // ---- activation quantisers (into shared memory) ----------------------------------------------
-// Q8_0: qs int8 [M][K], d (f16-rounded, as float) [M][K/32]. Each warp quantises blocks
-// warp, warp+8, ... in rounds of R blocks whose loads are all issued before any reduction.
+// 32 consecutive activation values of row m starting at k0 (16-byte loads when aligned).
 template <int PRO>
-__device__ void quantize_q8_0(const GemvParams & p, int8_t * xq, float * xd, double * red) {
-    constexpr int R    = 8;
-    const int     lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int     nb   = p.K / 32;
-    for (int m = 0; m < p.M; m++) {
-        const float sc = PRO == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
-        for (int b0 = warp; b0 < nb; b0 += kConsumerWarps * R) {
-            ActRaw<PRO> raw[R];
+__device__ __forceinline__ void act_block32(const GemvParams & p, int m, int k0, float sc, bool vec, float * v) {
+    const float * row = p.x + (int64_t) m * p.x_stride;
+    if (vec) {
+        float4 a[8], b[8];
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int b = b0 + r * kConsumerWarps;
-                if (b < nb) {
-                    raw[r] = act_load<PRO>(p, m, b * 32 + lane);
+        for (int i = 0; i < 8; i++) {
+            a[i] = *reinterpret_cast<const float4 *>(row + k0 + 4 * i);
+        }
+        if (PRO == PRO_SUM_SPLITS) {
+            for (int s = 1; s < p.n_split; s++) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    b[i] = *reinterpret_cast<const float4 *>(row + (int64_t) s * p.K + k0 + 4 * i);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    a[i].x = __fadd_rn(a[i].x, b[i].x);
+                    a[i].y = __fadd_rn(a[i].y, b[i].y);
+                    a[i].z = __fadd_rn(a[i].z, b[i].z);
+                    a[i].w = __fadd_rn(a[i].w, b[i].w);
                 }
             }
+        } else if (PRO == PRO_SWIGLU) {
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int b = b0 + r * kConsumerWarps;
-                if (b < nb) {
-                    const float v    = act_finish<PRO>(p, raw[r], sc);
-                    const float amax = warp_max(fabsf(v));
-                    const float d    = amax / 127.0f;
-                    const float id   = d != 0.0f ? 1.0f / d : 0.0f;
-                    xq[(int64_t) m * p.K + b * 32 + lane] = (int8_t) roundf(__fmul_rn(v, id));
-                    if (lane == 0) {
-                        xd[m * nb + b] = __half2float(__float2half_rn(d));
-                    }
-                }
+            for (int i = 0; i < 8; i++) {
+                b[i] = *reinterpret_cast<const float4 *>(row + p.K + k0 + 4 * i);
             }
+        } else if (PRO == PRO_RMSNORM && p.norm_w) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                b[i] = __ldg(reinterpret_cast<const float4 *>(p.norm_w + k0 + 4 * i));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float aa[4] = { a[i].x, a[i].y, a[i].z, a[i].w };
+            const float bb[4] = { b[i].x, b[i].y, b[i].z, b[i].w };
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                ActRaw<PRO> r{ aa[e], (PRO == PRO_RMSNORM && !p.norm_w) ? 1.0f : bb[e] };
+                v[4 * i + e] = act_finish<PRO>(p, r, sc);
+            }
+        }
+    } else {
+#pragma unroll 8
+        for (int e = 0; e < 32; e++) {
+            v[e] = act_finish<PRO>(p, act_load<PRO>(p, m, k0 + e), sc);
         }
     }
 }
 
-// Q8_K: qs int8 [M][K], d float [M][K/256], bsums int [M][K/16]
+// Q8_0: qs int8 [M][K], d (f16-rounded, as float) [M][K/32]. One consumer thread quantises one
+// whole 32-element block (no cross-lane reductions on the critical path).
 template <int PRO>
-__device__ void quantize_q8_K(const GemvParams & p, int8_t * xq, float * xd, int * xbs, double * red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nsb  = p.K / 256;
+__device__ void quantize_q8_0(const GemvParams & p, int8_t * xq, float * xd, double * red) {
+    const int  tid = threadIdx.x;
+    const int  nb  = p.K / 32;
+    const bool vec = (p.x_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
+                     (p.norm_w == nullptr || (reinterpret_cast<uintptr_t>(p.norm_w) & 15) == 0);
     for (int m = 0; m < p.M; m++) {
         const float sc = PRO == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
-        for (int sb = warp; sb < nsb; sb += kConsumerWarps) {
-            float v[8];
+        for (int b = tid; b < nb; b += kConsumerWarps * 32) {
+            float v[32];
+            act_block32<PRO>(p, m, b * 32, sc, vec, v);
+            float amax = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                amax = fmaxf(amax, fabsf(v[e]));
+            }
+            const float d  = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            uint32_t    w[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                uint32_t u = 0;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int q = (int) roundf(__fmul_rn(v[4 * i + e], id));
+                    u |= ((uint32_t) (q & 0xff)) << (8 * e);
+                }
+                w[i] = u;
+            }
+            uint4 * dst = reinterpret_cast<uint4 *>(xq + (int64_t) m * p.K + b * 32);
+            dst[0]      = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1]      = make_uint4(w[4], w[5], w[6], w[7]);
+            xd[m * nb + b] = __half2float(__float2half_rn(d));
+        }
+    }
+}
+
+// Q8_K: qs int8 [M][K], d float [M][K/256], bsums int [M][K/16]. Eight consumer threads share
+// a 256-element block, one 32-element part each; the signed maximum (first index on ties) is
+// combined over the eight with shuffles.
+template <int PRO>
+__device__ void quantize_q8_K(const GemvParams & p, int8_t * xq, float * xd, int * xbs, double * red) {
+    const int  tid  = threadIdx.x;
+    const int  part = tid & 7;
+    const int  nsb  = p.K / 256;
+    const bool vec  = (p.x_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
+                     (p.norm_w == nullptr || (reinterpret_cast<uintptr_t>(p.norm_w) & 15) == 0);
+    const int  rounds = (nsb + (kConsumerWarps * 4) - 1) / (kConsumerWarps * 4);
+    for (int m = 0; m < p.M; m++) {
+        const float sc = PRO == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
+        for (int r = 0; r < rounds; r++) {
+            const int  sb    = r * kConsumerWarps * 4 + (tid >> 3);
+            const bool valid = sb < nsb;
+            float      v[32];
+            if (valid) {
+                act_block32<PRO>(p, m, sb * 256 + part * 32, sc, vec, v);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    v[e] = 0.0f;
+                }
+            }
             float amax = 0.0f, mx = 0.0f;
             int   idx  = 0x7fffffff;
-            ActRaw<PRO> raw[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                raw[j] = act_load<PRO>(p, m, sb * 256 + lane * 8 + j);
-            }
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                v[j]         = act_finish<PRO>(p, raw[j], sc);
-                const float a = fabsf(v[j]);
+            for (int e = 0; e < 32; e++) {
+                const float a = fabsf(v[e]);
                 if (a > amax) {  // first index of the largest magnitude wins
                     amax = a;
-                    mx   = v[j];
-                    idx  = lane * 8 + j;
+                    mx   = v[e];
+                    idx  = part * 32 + e;
                 }
             }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
+            for (int o = 1; o < 8; o <<= 1) {
                 const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
                 const float om = __shfl_xor_sync(0xffffffffu, mx, o);
                 const int   oi = __shfl_xor_sync(0xffffffffu, idx, o);
@@ -193,29 +259,38 @@ __device__ void quantize_q8_K(const GemvParams & p, int8_t * xq, float * xd, int
                     idx  = oi;
                 }
             }
-            int8_t * q = xq + (int64_t) m * p.K + sb * 256 + lane * 8;
-            int      s = 0;
-            if (amax == 0.0f) {
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    q[j] = 0;
-                }
-            } else {
-                const float iscale = -127.0f / mx;
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    int iv = __float2int_rn(__fmul_rn(iscale, v[j]));
-                    iv     = iv < 127 ? iv : 127;
-                    q[j]   = (int8_t) iv;
-                    s += iv;
-                }
+            if (!valid) {
+                continue;
             }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);  // lanes 2g, 2g+1 hold group g
-            if ((lane & 1) == 0) {
-                xbs[m * (p.K / 16) + sb * 16 + lane / 2] = s;
+            uint32_t w[8];
+            int      s0 = 0, s1 = 0;
+            const float iscale = amax == 0.0f ? 0.0f : -127.0f / mx;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                uint32_t u = 0;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    int q = 0;
+                    if (amax != 0.0f) {
+                        q = __float2int_rn(__fmul_rn(iscale, v[4 * i + e]));
+                        q = q < 127 ? q : 127;
+                    }
+                    if (i < 4) {
+                        s0 += q;
+                    } else {
+                        s1 += q;
+                    }
+                    u |= ((uint32_t) (q & 0xff)) << (8 * e);
+                }
+                w[i] = u;
             }
-            if (lane == 0) {
-                xd[m * nsb + sb] = amax == 0.0f ? 0.0f : 1.0f / (-127.0f / mx);
+            uint4 * dst = reinterpret_cast<uint4 *>(xq + (int64_t) m * p.K + sb * 256 + part * 32);
+            dst[0]      = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1]      = make_uint4(w[4], w[5], w[6], w[7]);
+            xbs[m * (p.K / 16) + sb * 16 + part * 2]     = s0;
+            xbs[m * (p.K / 16) + sb * 16 + part * 2 + 1] = s1;
+            if (part == 0) {
+                xd[m * nsb + sb] = amax == 0.0f ? 0.0f : 1.0f / iscale;
             }
         }
     }

@@ -96,7 +96,7 @@ struct acb_qw3lm {
     size_t               layer_elems = 0;
     int                  cap_tok     = 0;
     int                  max_split   = 1;
-    DevBuf hidden, qkv, q, scores, smax, part, gu, logits, ids, pos, err, hist_base, hist, mhist, amax;
+    DevBuf hidden, qkv, q, scores, smax, part, att, tickets, gu, logits, ids, pos, err, hist_base, hist, mhist, amax;
     int32_t *                           h_ids = nullptr;
     int32_t *                           h_pos = nullptr;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -181,9 +181,9 @@ acb_status enqueue_layers(acb_qw3lm * m, int n, int set0, int set_per_tok) {
         const int ns = m->splits(n);
         ACB_TRY(acb_attn_decode(m->q.as<float>(), qd, n, c.n_heads, c.n_kv_heads, D, m->pos.as<int32_t>(), kc, vc,
                                 c.max_seq_len, set0, set_per_tok, 1.0f / sqrtf((float) D), ns, m->scores.as<float>(),
-                                m->smax.as<float>(), m->part.as<float>(), ACB_FLAG_PDL, (acb_stream_t) m->st));
-        ACB_TRY(gemv_rows(m, L.o, 0, H, n, ACB_PRO_SUM_SPLITS, m->part.as<float>(), (int64_t) ns * qd, nullptr, ns, hid,
-                          H, ACB_EPI_ADD, hid, H));
+                                m->smax.as<float>(), m->part.as<float>(), m->att.as<float>(), qd,
+                                m->tickets.as<int>(), ACB_FLAG_PDL, (acb_stream_t) m->st));
+        ACB_TRY(gemv_rows(m, L.o, 0, H, n, ACB_PRO_X, m->att.as<float>(), qd, nullptr, 0, hid, H, ACB_EPI_ADD, hid, H));
         const float * pn = (const float *) L.post_norm->data;
         float *       gu = m->gu.as<float>();
         if (L.gate_up) {
@@ -411,6 +411,8 @@ extern "C" acb_status acb_qw3lm_load(const char * gguf_path, int max_seq_len, in
     f |= m->scores.alloc(T * c.n_heads * (size_t) S * 4) != ACB_OK;
     f |= m->smax.alloc(T * c.n_heads * m->max_split * 4) != ACB_OK;
     f |= m->part.alloc(part_n * m->qd() * 4) != ACB_OK;
+    f |= m->att.alloc(T * m->qd() * 4) != ACB_OK;
+    f |= m->tickets.alloc(T * c.n_kv_heads * 4) != ACB_OK;  // zeroed; every attention call leaves it zero
     f |= m->gu.alloc(T * 2 * c.intermediate_size * 4) != ACB_OK;
     f |= m->logits.alloc((size_t) kMaxSets * c.vocab_size * 4) != ACB_OK;
     f |= m->ids.alloc(T * 4) != ACB_OK;

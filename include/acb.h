@@ -185,13 +185,16 @@ ACB_API int acb_attn_decode_splits(int n_tok, int Nkv);
 /* One-token attention for n_tok sequences over the f16 cache, kv_len = pos[t] + 1, with
  * ggml-CPU semantics (q and normalised probabilities rounded to f16, softmax sum in double).
  * Scratch (device, caller-owned): scores [n_tok][Nh][max_seq] f32, smax [n_tok][Nh][n_split]
- * f32; output: part [n_tok][n_split][Nh*128] f32 split partials, summed by the O-projection's
- * ACB_PRO_SUM_SPLITS prologue. Replaces ggml_flash_attn_ext / qwen3_attn_f32 on the cache view
- * (src/qwen3-lm.h:705-723). */
+ * f32, part [n_tok][n_split][Nh*128] f32 split partials. With out (and tickets, int
+ * [n_tok][Nkv], zeroed before first use and returned to zero by every call) the last split CTA
+ * of each (token, kv head) sums the partials in split order into out[t*out_stride + h*128 + d];
+ * with out NULL the partials are left for the O-projection's ACB_PRO_SUM_SPLITS prologue.
+ * Replaces ggml_flash_attn_ext / qwen3_attn_f32 on the cache view (src/qwen3-lm.h:705-723). */
 ACB_API acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok, int Nh, int Nkv, int head_dim,
                                    const int32_t * pos, const uint16_t * k_cache, const uint16_t * v_cache,
                                    int max_seq, int set0, int set_per_tok, float scale, int n_split, float * scores,
-                                   float * smax, float * part, int flags, acb_stream_t stream);
+                                   float * smax, float * part, float * out, int64_t out_stride, int * tickets,
+                                   int flags, acb_stream_t stream);
 
 /* Device scratch (bytes) acb_argmax needs for `rows` rows of V logits. */
 ACB_API size_t acb_argmax_scratch_bytes(int rows, int64_t V);
