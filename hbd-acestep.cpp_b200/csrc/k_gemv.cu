@@ -24,6 +24,7 @@ enum { EPI_STORE = 0, EPI_ADD = 1 };
 
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads       = (kConsumerWarps + 1) * 32;
+constexpr int kHdr           = 256;  // shared-memory header bytes (barriers, reduction)
 
 struct GemvParams {
     const uint8_t * W;
@@ -480,17 +481,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // shared layout: [barriers][reduction][x quants][x scales][x bsums][stages]
+    // header: full[8] @0, empty[8] @64, reduction doubles[8] @128, activation from 256
     uint64_t * full  = reinterpret_cast<uint64_t *>(smem);
-    uint64_t * empty = full + 4;
-    double *   red   = reinterpret_cast<double *>(smem + 64);
-    int8_t *   xq    = reinterpret_cast<int8_t *>(smem + 128);
+    uint64_t * empty = full + 8;
+    double *   red   = reinterpret_cast<double *>(smem + 128);
+    int8_t *   xq    = reinterpret_cast<int8_t *>(smem + kHdr);
     const int  xq_bytes = (MT * p.K + 15) / 16 * 16;
-    float *    xd       = reinterpret_cast<float *>(smem + 128 + xq_bytes);
+    float *    xd       = reinterpret_cast<float *>(smem + kHdr + xq_bytes);
     const int  nscale   = QT == ACB_TYPE_Q8_0 ? p.K / 32 : p.K / 256;
     const int  xd_bytes = (MT * nscale * 4 + 15) / 16 * 16;
-    int *      xbs      = reinterpret_cast<int *>(smem + 128 + xq_bytes + xd_bytes);
+    int *      xbs      = reinterpret_cast<int *>(smem + kHdr + xq_bytes + xd_bytes);
     const int  bs_bytes = QT == ACB_TYPE_Q8_0 ? 0 : (MT * (p.K / 16) * 4 + 15) / 16 * 16;
-    const int  st_off   = (128 + xq_bytes + xd_bytes + bs_bytes + 127) / 128 * 128;
+    const int  st_off   = (kHdr + xq_bytes + xd_bytes + bs_bytes + 127) / 128 * 128;
     uint8_t *  stages   = smem + st_off;
 
     const int64_t row0   = (int64_t) blockIdx.x * p.rows_per_cta;
@@ -608,10 +610,13 @@ static acb_status launch_gemv(GemvParams p, bool pdl, cudaStream_t st) {
     const int xq_bytes = (MT * p.K + 15) / 16 * 16;
     const int xd_bytes = (MT * nscale * 4 + 15) / 16 * 16;
     const int bs_bytes = QT == ACB_TYPE_Q8_0 ? 0 : (MT * (p.K / 16) * 4 + 15) / 16 * 16;
-    const int st_off   = (128 + xq_bytes + xd_bytes + bs_bytes + 127) / 128 * 128;
+    const int st_off   = (kHdr + xq_bytes + xd_bytes + bs_bytes + 127) / 128 * 128;
     const int64_t chunks_per_cta = (per_cta + chunk - 1) / chunk;
-    int stages = chunks_per_cta < 4 ? (int) chunks_per_cta : 4;
-    while (stages > 1 && st_off + (int64_t) stages * p.stage_bytes > 110 * 1024) {
+    // deep rings for long row ranges (bytes in flight cover the loaded-HBM latency), shallow
+    // ones for short ranges so a CTA of the next kernel can co-reside
+    int stages = chunks_per_cta < 6 ? (int) chunks_per_cta : 6;
+    const int64_t smem_cap = chunks_per_cta > 4 ? 200 * 1024 : 110 * 1024;
+    while (stages > 1 && st_off + (int64_t) stages * p.stage_bytes > smem_cap) {
         stages--;
     }
     p.stages = stages < 1 ? 1 : stages;
