@@ -7,6 +7,9 @@
 // (best, index, second) triple. Partials go to caller-provided scratch; the CTA that finishes
 // last (ticket counter, which it resets for the next launch) merges them and writes the token,
 // so the whole sampling step is one launch and can sit inside a CUDA graph.
+#include <mutex>
+#include <string>
+
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -152,6 +155,36 @@ static int argmax_blocks(int64_t V) {
     return (int) (n < 1 ? 1 : (n > 128 ? 128 : n));
 }
 
+static acb_status launch_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
+                                float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
+                                int64_t hist_stride, const int32_t * hist_base, void * scratch, int flags,
+                                cudaStream_t stream) {
+    const int nblk  = argmax_blocks(V);
+    int64_t   chunk = (V + nblk - 1) / nblk;
+    chunk           = (chunk + 3) / 4 * 4;
+    float4 *  part   = reinterpret_cast<float4 *>(scratch);
+    int *     ticket = reinterpret_cast<int *>(part + (size_t) rows * nblk);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) nblk, (unsigned) rows);
+    cfg.blockDim           = dim3(256);
+    cfg.stream             = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const bool pdl                                     = flags & 1;
+    cfg.attrs                                          = pdl ? attr : nullptr;
+    cfg.numAttrs                                       = pdl ? 1 : 0;
+    cudaError_t e = pdl ? cudaLaunchKernelEx(&cfg, argmax_kernel<1>, logits, stride, V, chunk, ids, margin,
+                                             pos_advance, hist, mhist, hist_stride, hist_base, part, ticket)
+                        : cudaLaunchKernelEx(&cfg, argmax_kernel<0>, logits, stride, V, chunk, ids, margin,
+                                             pos_advance, hist, mhist, hist_stride, hist_base, part, ticket);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
 }  // namespace acb
 
 using namespace acb;
@@ -174,29 +207,74 @@ extern "C" acb_status acb_argmax(const float * logits, int64_t stride, int64_t V
     if (reinterpret_cast<uintptr_t>(scratch) % 16 != 0) {
         return ACB_ERR_INVALID_ARG;
     }
-    const int     nblk   = argmax_blocks(V);
-    int64_t       chunk  = (V + nblk - 1) / nblk;
-    chunk                = (chunk + 3) / 4 * 4;
-    float4 *      part   = reinterpret_cast<float4 *>(scratch);
-    int *         ticket = reinterpret_cast<int *>(part + (size_t) rows * nblk);
-    const dim3    grid((unsigned) nblk, (unsigned) rows);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim            = grid;
-    cfg.blockDim           = dim3(256);
-    cfg.stream             = (cudaStream_t) stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    const bool pdl                                     = flags & 1;
-    cfg.attrs                                          = pdl ? attr : nullptr;
-    cfg.numAttrs                                       = pdl ? 1 : 0;
-    cudaError_t e = pdl ? cudaLaunchKernelEx(&cfg, argmax_kernel<1>, logits, stride, V, chunk, ids, margin,
-                                             pos_advance, hist, mhist, hist_stride, hist_base, part, ticket)
-                        : cudaLaunchKernelEx(&cfg, argmax_kernel<0>, logits, stride, V, chunk, ids, margin,
-                                             pos_advance, hist, mhist, hist_stride, hist_base, part, ticket);
-    if (e != cudaSuccess) {
-        set_last_cuda_error(e);
+    return launch_argmax(logits, stride, V, rows, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base,
+                         scratch, flags, (cudaStream_t) stream);
+}
+
+// ---- variant with library-owned scratch (no allocation by the caller or the library) ------------
+//
+// For callers that cannot allocate device memory at the point where they sample: a host that
+// hands the whole device to its own memory pool (and forbids allocations behind its back), or a
+// latency-critical decode thread that must not call cudaMalloc because it can synchronise the
+// device. The scratch lives in a fixed array in this module's device memory instead; every
+// device that loads the library holds it (ACB_ARGMAX_NOALLOC_MAX_ROWS rows) until the process
+// exits.
+namespace acb {
+constexpr int    kNoallocRows  = ACB_ARGMAX_NOALLOC_MAX_ROWS;
+constexpr size_t kNoallocBytes = ((size_t) kNoallocRows * 128 * sizeof(float4) + kNoallocRows * sizeof(int) + 255) /
+                                 256 * 256;
+static __device__ __align__(256) unsigned char g_argmax_scratch[kNoallocBytes];
+
+// Device address of g_argmax_scratch per device ordinal. In host code the array's name is only a
+// host-side stand-in, so the address is looked up once per device, with that device current.
+static void *     g_scratch_addr[64];
+static std::mutex g_scratch_mu;
+
+void set_last_error(const std::string & e);
+
+static acb_status noalloc_scratch(void ** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         return ACB_ERR_CUDA;
     }
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        void *            p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
+        if (e != cudaSuccess || !p) {
+            set_last_cuda_error(e);
+            set_last_error("acb_argmax_noalloc: cudaGetSymbolAddress failed");
+            return ACB_ERR_CUDA;
+        }
+        // the ticket counters must start at zero; every call returns them to zero
+        if (cudaMemset(p, 0, kNoallocBytes) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
     return ACB_OK;
+}
+}  // namespace acb
+
+extern "C" acb_status acb_argmax_noalloc(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
+                                         float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
+                                         int64_t hist_stride, const int32_t * hist_base, int flags,
+                                         acb_stream_t stream) {
+    if (!logits || !ids || V <= 0 || V > INT32_MAX || rows <= 0 || stride < V ||
+        (hist && (!pos_advance || !hist_base))) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (rows > kNoallocRows || acb_argmax_scratch_bytes(rows, V) > kNoallocBytes) {
+        set_last_error("acb_argmax_noalloc: rows exceeds ACB_ARGMAX_NOALLOC_MAX_ROWS (" +
+                       std::to_string(kNoallocRows) + "); use acb_argmax with caller scratch");
+        return ACB_ERR_UNSUPPORTED;
+    }
+    void *     scratch = nullptr;
+    acb_status st      = noalloc_scratch(&scratch);
+    if (st != ACB_OK) {
+        return st;
+    }
+    return launch_argmax(logits, stride, V, rows, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base,
+                         scratch, flags, (cudaStream_t) stream);
 }

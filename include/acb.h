@@ -212,6 +212,23 @@ ACB_API acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, i
                               int32_t * pos_advance, int32_t * hist, float * mhist, int64_t hist_stride,
                               const int32_t * hist_base, void * scratch, int flags, acb_stream_t stream);
 
+/* acb_argmax for callers that cannot allocate device memory when they sample: a host whose own
+ * pool owns the whole device and forbids allocations it did not make, or a decode thread that
+ * must never call cudaMalloc because it can synchronise the device. No counterpart in the
+ * reference (which samples on the host). Same arguments and results as acb_argmax without
+ * `scratch`: the scratch is a fixed array in the library's device memory, sized for
+ * ACB_ARGMAX_NOALLOC_MAX_ROWS rows of any vocabulary, which every device that loads the
+ * library holds until the process exits. More rows return ACB_ERR_UNSUPPORTED (message in
+ * acb_last_error) without launching anything. Nothing is allocated by the call. The first call
+ * on each device looks up the array's device address and clears it, so make that first call
+ * outside any stream capture; afterwards every call leaves the array reusable. All calls on a
+ * device share the array: calls that overlap on the GPU (different streams, no ordering) race
+ * and must be serialised by the caller. */
+#define ACB_ARGMAX_NOALLOC_MAX_ROWS 32
+ACB_API acb_status acb_argmax_noalloc(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
+                                      float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
+                                      int64_t hist_stride, const int32_t * hist_base, int flags, acb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
