@@ -291,6 +291,9 @@ def run_ours(args):
     if args.workloads == "gemv":
         print(json.dumps(run_gemv_shapes(dev)), flush=True)
         return
+    if args.workloads == "gemm":
+        print(json.dumps(run_gemm_shapes(dev)), flush=True)
+        return
     if "ops" not in args.workloads.split(","):
         # LM-only run (profiling): one line with the decode result
         lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt, gen_len=args.lm_gen)
@@ -446,6 +449,40 @@ def run_gemv_shapes(dev, reps=20):
         nbytes = N * rb + K * 4 + N * 4
         out["shapes"][name] = {"N": N, "K": K, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1)}
         del W
+    return out
+
+
+# ---- tcgen05 GEMM at the DiT layer shapes (M = 8 sequences x 750 tokens) -----------------------
+
+GEMM_SHAPES = [("sa_qkv", 6000, 4096, 2048), ("sa_o", 6000, 2048, 2048), ("gate_up", 6000, 12288, 2048),
+               ("down", 6000, 2048, 6144)]
+
+
+def run_gemm_shapes(dev, reps=20):
+    """acb_gemm_bf16 (bf16 in, f32 accumulate, bf16 out) per DiT linear shape, CUDA events around
+    `reps` launches after 3 warm-ups; TFLOP/s against the measured bf16 peak."""
+    import torch
+
+    import acb
+    peaks, kind = measured_peaks()
+    out = {"metric": "tcgen05 bf16 GEMM TFLOP/s per DiT shape", "peak_tflops": peaks["bf16_tflops"],
+           "peak_kind": kind, "shapes": {}}
+    for name, M, N, K in GEMM_SHAPES:
+        A = torch.randn(M, K, device=dev).bfloat16()
+        B = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+        C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            acb.gemm_bf16(A, B, out=C)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            acb.gemm_bf16(A, B, out=C)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+        out["shapes"][name] = {"M": M, "N": N, "K": K, "us": round(us, 1), "TFLOP/s": round(tf, 1),
+                               "frac": round(tf / peaks["bf16_tflops"], 3)}
     return out
 
 

@@ -66,6 +66,7 @@ def lib():
             "acb_gated_residual": (I, [P, P, I, P, I64, P, I64, I64, I, P]),
             "acb_get_rows": (I, [P, I, I64, I64, P, I64, P, I, I64, P, P]),
             "acb_quantize": (I, [P, I64, I64, I, P, P]),
+            "acb_gemm_bf16": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, P]),
             "acb_gemv": (I, [P, I, I64, I64, I, I, P, I64, P, F, I, P, I64, I, P, I64, I, P, P]),
             "acb_qkv_post": (I, [P, I64, I64, I, I, I, P, P, F, P, P, I, P, I64, P, P, I, I, I, I, P, P]),
             "acb_attn_decode_splits": (I, [I, I]),
@@ -342,3 +343,21 @@ class QW3LM:
             self.h, last.ctypes.data, set0, N, n_steps, toks.ctypes.data,
             None if marg is None else marg.ctypes.data, C.byref(ms)))
         return toks, marg, ms.value
+
+
+# ---- dense path ------------------------------------------------------------------------------------
+
+def gemm_bf16(A, B, out=None, out_dtype=None, bias=None, res=None, gate=None, rows_per_sample=None, flags=0,
+              err=None, stream=None):
+    """C = A @ B.T (+ bias) (res + C or res + C * gate) on tcgen05. A [M,K], B [N,K] bf16 CUDA tensors."""
+    import torch
+    M, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or torch.float32, device=A.device)
+    gs = 0 if gate is None else (gate.stride(0) if gate.dim() > 1 else 0)
+    _check("acb_gemm_bf16", lib().acb_gemm_bf16(
+        _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, N, K, _ptr(out), dtype_id(out), out.stride(0), _ptr(bias),
+        _ptr(res), res.stride(0) if res is not None else 0, _ptr(gate), gs, rows_per_sample or M, flags, _ptr(err),
+        _stream(stream)))
+    return out

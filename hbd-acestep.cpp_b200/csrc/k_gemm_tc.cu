@@ -1,0 +1,404 @@
+// k_gemm_tc.cu -- tensor-core GEMM for the dense prefill / DiT linears (src/dit-graph.h:36-49 and
+// every ggml_mul_mat of dit_ggml_build_layer at M = tokens):
+//     C[m][n] = epilogue( sum_k A[m][k] * B[n][k] ),  A, B bf16 K-major, fp32 accumulation.
+//
+// sm_100a design (one persistent CTA per SM, 6 warps, no clusters, no multicast):
+//   warp 0      TMA producer: A tile 128x64 and B tile 256x64 per stage (128-byte swizzle) into a
+//               4-stage ring (48 KB per stage), completion on an mbarrier per stage;
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators), one elected thread
+//               issues tcgen05.mma (M=128, N=256, K=16; kind::f16 with bf16 inputs) and releases
+//               ring stages / publishes finished accumulators with tcgen05.commit;
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quarter, fused
+//               bias / residual / DiT gated residual, bf16 or f32 stores; the accumulator is
+//               handed back so the MMA of the next tile overlaps this epilogue.
+// Every mbarrier wait is bounded; on a timeout the kernel records ACB_DEVERR_TIMEOUT, stops, and
+// still frees its TMEM.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace acb {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
+constexpr int kATile = kBM * kBK * 2;  // 16 KB
+constexpr int kBTile = kBN * kBK * 2;  // 32 KB
+constexpr int kStageBytes = kATile + kBTile;
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols    = 512;
+
+enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RES = 2, EPI_GATED_RES = 4 };
+
+struct GemmArgs {
+    int64_t       M, N, K;
+    void *        C;
+    int           c_type;  // ACB_TYPE_F32 or ACB_TYPE_BF16
+    int64_t       ldc;
+    const float * bias;    // [N] or null
+    int           epi;     // bit set of EPI_*
+    const float * res;     // f32 [M][ldr] (may alias C when C is f32)
+    int64_t       ldr;
+    const float * gate;    // f32 [samples][gate_stride], EPI_GATED_RES: C = res + acc * gate
+    int64_t       gate_stride;
+    int64_t       rows_per_sample;
+    int *         err;
+};
+
+// ---- tcgen05 / TMA helpers ------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            ptx::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(ptx::smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap * map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart (SM100 shared-memory descriptor:
+// start >> 4 at [0,14), stride byte offset >> 4 at [32,46), version 1 at [46,48), layout 2 at [61,64)).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    return (uint64_t) ((saddr & 0x3FFFF) >> 4) | ((uint64_t) (1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128, N=256.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     ptx::smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t * r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+        "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void flag_timeout(int * err) {
+    if (err) {
+        atomicOr(err, ACB_DEVERR_TIMEOUT);
+    }
+}
+
+// ---- the kernel ------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const GemmArgs g) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t * ring = smem;  // kStages * kStageBytes, 1024-aligned tiles
+    uint64_t * full       = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
+    uint64_t * empty      = full + kStages;
+    uint64_t * tmem_full  = empty + kStages;
+    uint64_t * tmem_empty = tmem_full + 2;
+    uint32_t * tmem_slot  = reinterpret_cast<uint32_t *>(tmem_empty + 2);
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m_tiles = (g.M + kBM - 1) / kBM, n_tiles = (g.N + kBN - 1) / kBN;
+    const int64_t n_work  = m_tiles * n_tiles;
+    const int     k_tiles = (int) (g.K / kBK);
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        for (int s = 0; s < kStages; s++) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            ptx::mbar_init(&tmem_full[a], 1);
+            ptx::mbar_init(&tmem_empty[a], 4);  // one arrival per epilogue warp
+        }
+        ptx::fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         ptx::smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    ptx::grid_dep_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int it = 0;  // global k-stage counter
+            for (int64_t w = blockIdx.x; w < n_work && !abort_flag; w += gridDim.x) {
+                const int m0 = (int) ((w % m_tiles) * kBM), n0 = (int) ((w / m_tiles) * kBN);
+                for (int kt = 0; kt < k_tiles; kt++, it++) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !ptx::mbar_wait(&empty[s], ((it / kStages) - 1) & 1)) {
+                        flag_timeout(g.err);
+                        abort_flag = 1;
+                        break;
+                    }
+                    uint8_t * st = ring + (size_t) s * kStageBytes;
+                    ptx::mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st, &tmA, kt * kBK, m0, &full[s]);
+                    tma_load_2d(st + kATile, &tmB, kt * kBK, n0, &full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16(kBM, kBN);
+            int                it    = 0;
+            int                tile  = 0;
+            for (int64_t w = blockIdx.x; w < n_work && !abort_flag; w += gridDim.x, tile++) {
+                const int acc = tile & 1;
+                if (tile >= 2 && !ptx::mbar_wait(&tmem_empty[acc], ((tile >> 1) - 1) & 1)) {
+                    flag_timeout(g.err);
+                    abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t) (acc * kBN);
+                for (int kt = 0; kt < k_tiles; kt++, it++) {
+                    const int s = it % kStages;
+                    if (!ptx::mbar_wait(&full[s], (it / kStages) & 1)) {
+                        flag_timeout(g.err);
+                        abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = ptx::smem_u32(ring + (size_t) s * kStageBytes);
+                    const uint32_t b0 = a0 + kATile;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; kk++) {
+                        umma_bf16(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                                  (kt | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                }
+                umma_commit(&tmem_full[acc]);  // accumulator complete
+            }
+        }
+    } else {
+        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = tile rows
+        const int q    = warp & 3;
+        const int row_in_tile = q * 32 + lane;
+        int       tile = 0;
+        for (int64_t w = blockIdx.x; w < n_work; w += gridDim.x, tile++) {
+            const int acc = tile & 1;
+            if (!ptx::mbar_wait(&tmem_full[acc], (tile >> 1) & 1)) {
+                if (lane == 0) {
+                    flag_timeout(g.err);
+                }
+                abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const int64_t m = (w % m_tiles) * kBM + row_in_tile;
+            const int64_t n0 = (w / m_tiles) * kBN;
+            const float * gate_row =
+                (g.epi & EPI_GATED_RES) ? g.gate + (m < g.M ? (m / g.rows_per_sample) : 0) * g.gate_stride : nullptr;
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; c++) {
+                uint32_t r[32];
+                tmem_ld32(tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN + c * 32), r);
+                const int64_t nc = n0 + c * 32;
+                if (m < g.M && nc < g.N) {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    v[j] = __uint_as_float(r[j]);
+                }
+                const bool full_cols = nc + 32 <= g.N;
+                if (g.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        if (full_cols || nc + j < g.N) {
+                            v[j] = __fadd_rn(v[j], g.bias[nc + j]);
+                        }
+                    }
+                }
+                if (g.epi & (EPI_RES | EPI_GATED_RES)) {
+                    const float * rr = g.res + m * g.ldr + nc;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        if (full_cols || nc + j < g.N) {
+                            const float o = (g.epi & EPI_GATED_RES) ? __fmul_rn(v[j], gate_row[nc + j]) : v[j];
+                            v[j]          = __fadd_rn(rr[j], o);
+                        }
+                    }
+                }
+                if (g.c_type == ACB_TYPE_F32) {
+                    float * dst = reinterpret_cast<float *>(g.C) + m * g.ldc + nc;
+                    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        }
+                    } else {
+                        for (int j = 0; j < 32 && nc + j < g.N; j++) {
+                            dst[j] = v[j];
+                        }
+                    }
+                } else {
+                    __nv_bfloat16 * dst = reinterpret_cast<__nv_bfloat16 *>(g.C) + m * g.ldc + nc;
+                    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            union {
+                                __nv_bfloat16 h[8];
+                                uint4         u;
+                            } pk;
+#pragma unroll
+                            for (int e = 0; e < 8; e++) {
+                                pk.h[e] = __float2bfloat16_rn(v[j + e]);
+                            }
+                            *reinterpret_cast<uint4 *>(dst + j) = pk.u;
+                        }
+                    } else {
+                        for (int j = 0; j < 32 && nc + j < g.N; j++) {
+                            dst[j] = __float2bfloat16_rn(v[j]);
+                        }
+                    }
+                }
+                }  // valid row and column chunk
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                ptx::mbar_arrive(&tmem_empty[acc]);
+            }
+        }
+    }
+    ptx::grid_dep_launch();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+    }
+}
+
+// ---- host: tensor maps through the driver entry point (no libcuda link) ----------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *                          p  = nullptr;
+        cudaDriverEntryPointQueryResult qr = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
+            qr == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    });
+    return fn;
+}
+
+// bf16 row-major [rows][ld] (K contiguous), box = box_rows x 64 elements, 128-byte swizzle
+static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) {
+        return false;
+    }
+    const cuuint64_t dims[2]    = { (cuuint64_t) K, (cuuint64_t) rows };
+    const cuuint64_t strides[1] = { (cuuint64_t) (ld * 2) };
+    const cuuint32_t box[2]     = { (cuuint32_t) kBK, (cuuint32_t) box_rows };
+    const cuuint32_t estr[2]    = { 1, 1 };
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
+                                    int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
+                                    int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
+                                    int flags, int * err_flag, acb_stream_t stream) {
+    if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || lda < K || ldb < K || ldc < N) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (K % kBK != 0 || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 || reinterpret_cast<uintptr_t>(A) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(B) % 16 != 0) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (c_type != ACB_TYPE_F32 && c_type != ACB_TYPE_BF16) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (gate && (!res || rows_per_sample <= 0)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    GemmArgs g        = {};
+    g.M               = M;
+    g.N               = N;
+    g.K               = K;
+    g.C               = C;
+    g.c_type          = c_type;
+    g.ldc             = ldc;
+    g.bias            = bias;
+    g.epi             = (bias ? EPI_BIAS : 0) | (gate ? EPI_GATED_RES : (res ? EPI_RES : 0));
+    g.res             = res;
+    g.ldr             = ldr;
+    g.gate            = gate;
+    g.gate_stride     = gate_stride;
+    g.rows_per_sample = rows_per_sample > 0 ? rows_per_sample : 1;
+    g.err             = err_flag;
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A, M, K, lda, kBM) || !make_map(&tb, B, N, K, ldb, kBN)) {
+        return ACB_ERR_CUDA;
+    }
+    const int64_t work = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int     grid = (int) (work < num_sms() ? work : num_sms());
+    const size_t  smem = (size_t) kStages * kStageBytes + 1024 + 256;
+    cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) grid);
+    cfg.blockDim           = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = (cudaStream_t) stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = (flags & 1) ? attr : nullptr;
+    cfg.numAttrs                                       = (flags & 1) ? 1 : 0;
+    const cudaError_t e                                = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel, ta, tb, g);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}

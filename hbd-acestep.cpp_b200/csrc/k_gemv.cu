@@ -22,7 +22,7 @@ namespace acb {
 enum { PRO_X = 0, PRO_RMSNORM = 1, PRO_SUM_SPLITS = 2, PRO_SWIGLU = 3 };
 enum { EPI_STORE = 0, EPI_ADD = 1 };
 
-constexpr int kConsumerWarps = 8;
+constexpr int kConsumerWarps = 16;
 constexpr int kThreads       = (kConsumerWarps + 1) * 32;
 constexpr int kHdr           = 256;  // shared-memory header bytes (barriers, reduction)
 
@@ -167,7 +167,7 @@ __device__ __forceinline__ void act_block32(const GemvParams & p, int m, int k0,
             }
         }
     } else {
-#pragma unroll 8
+#pragma unroll
         for (int e = 0; e < 32; e++) {
             v[e] = act_finish<PRO>(p, act_load<PRO>(p, m, k0 + e), sc);
         }

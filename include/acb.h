@@ -136,6 +136,23 @@ ACB_API acb_status acb_get_rows(const void * table, int table_type, int64_t n_ro
  * on device (the reference requantises on the host in src/adapter-merge.h:357-472). */
 ACB_API acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int type, void * dst, acb_stream_t stream);
 
+/* ---- dense path (configs 1, 4, 5): tensor-core GEMM ---------------------------------------- */
+
+/* C[m][n] = epi(sum_k A[m][k] B[n][k]) on the 5th-generation tensor cores (tcgen05.mma, TMEM
+ * accumulators, TMA-fed 128-byte-swizzled tiles): A [M][lda] and B [N][ldb] bf16 row-major
+ * (K contiguous, K a multiple of 64, rows 16-byte aligned), fp32 accumulation, C f32 or bf16
+ * [M][ldc]. Epilogue, applied in order: + bias[n] (f32, optional); then with res (f32 [M][ldr],
+ * may alias an f32 C): C = res + acc, or with gate (f32, row m uses gate[(m / rows_per_sample) *
+ * gate_stride + n]): C = res + acc * gate, the DiT gated residual. B holds the weights
+ * dequantised once to bf16 (acb_get_rows with identity ids). Replaces ggml_mul_mat at M = tokens
+ * in dit_ggml_linear(_bias) (src/dit-graph.h:36-49), the DiT layer's projections
+ * (dit-graph.h:159-172, 258-268, 298-314) with dit_ggml_gated_add (:70-76) fused, and the
+ * encoder's prefill linears (src/qwen3-enc.h:86-88). */
+ACB_API acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
+                                 int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
+                                 int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
+                                 int flags, int * err_flag, acb_stream_t stream);
+
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 
 enum {

@@ -1,0 +1,63 @@
+"""GPU: the tcgen05 tensor-core GEMM (acb_gemm_bf16) against a plain PyTorch fp32 reference of
+the same op on the same bf16 operands. Only the fp32 accumulation order differs, so the bar is
+max_rel <= 1e-5 (relative to max |C|) for f32 output and one bf16 rounding step for bf16 output.
+Shapes cover single tiles, ragged M/N tails, the DiT layer shapes at 8 x 750 tokens and K=6144."""
+import numpy as np
+import pytest
+
+import acb
+from helpers import max_rel
+
+pytestmark = pytest.mark.gpu
+
+
+def ref_mm(A, B):
+    """fp32 reference (TF32 off) of the same bf16 operands."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    return A.float() @ B.float().T
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (77, 300, 128), (129, 257, 192),
+                                   (6000, 4096, 2048), (6000, 2048, 6144), (1, 256, 64)])
+def test_gemm_plain(cuda, M, N, K):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + N + K)
+    A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    C = acb.gemm_bf16(A, B, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = ref_mm(A, B)
+    r = max_rel(C.cpu().numpy(), ref.cpu().numpy())
+    assert r <= 1e-5, r
+
+
+def test_gemm_epilogues(cuda):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(3)
+    S, T, K, N = 4, 250, 512, 768
+    M = S * T
+    A = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+    bias = torch.randn(N, device=cuda, generator=g)
+    res = torch.randn(M, N, device=cuda, generator=g)
+    gate = torch.randn(S, N, device=cuda, generator=g)
+    base = ref_mm(A, B)
+    # bias only, f32
+    C = acb.gemm_bf16(A, B, bias=bias)
+    assert max_rel(C.cpu().numpy(), (base + bias).cpu().numpy()) <= 1e-5
+    # residual add (in place on an f32 buffer aliasing res)
+    out = res.clone()
+    acb.gemm_bf16(A, B, out=out, res=out)
+    assert max_rel((out - res).cpu().numpy(), base.cpu().numpy()) <= 1e-5
+    # DiT gated residual: res + (acc + bias) * gate[sample]
+    out = res.clone()
+    acb.gemm_bf16(A, B, out=out, bias=bias, res=out, gate=gate, rows_per_sample=T)
+    want = res + (base + bias) * gate.repeat_interleave(T, dim=0)
+    assert max_rel((out - res).cpu().numpy(), (want - res).cpu().numpy()) <= 1e-5
+    # bf16 output
+    Cb = acb.gemm_bf16(A, B, out_dtype=torch.bfloat16)
+    d = (Cb.float() - base).abs()
+    assert (d <= base.abs() * 2.0 ** -8 + 1e-6).all()
