@@ -67,6 +67,8 @@ def lib():
             "acb_get_rows": (I, [P, I, I64, I64, P, I64, P, I, I64, P, P]),
             "acb_quantize": (I, [P, I64, I64, I, P, P]),
             "acb_gemm_bf16": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, P]),
+            "acb_attn_prefill": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I, I,
+                                     I, F, I, P]),
             "acb_gemv": (I, [P, I, I64, I64, I, I, P, I64, P, F, I, P, I64, I, P, I64, I, P, P]),
             "acb_qkv_post": (I, [P, I64, I64, I, I, I, P, P, F, P, P, I, P, I64, P, P, I, I, I, I, P, P]),
             "acb_attn_decode_splits": (I, [I, I]),
@@ -360,4 +362,24 @@ def gemm_bf16(A, B, out=None, out_dtype=None, bias=None, res=None, gate=None, ro
         _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, N, K, _ptr(out), dtype_id(out), out.stride(0), _ptr(bias),
         _ptr(res), res.stride(0) if res is not None else 0, _ptr(gate), gs, rows_per_sample or M, flags, _ptr(err),
         _stream(stream)))
+    return out
+
+
+MASK_NONE, MASK_CAUSAL, MASK_WINDOW = 0, 1, 2
+
+
+def attn_prefill(q, k, v, Nh, Nkv, mask=MASK_NONE, window=0, causal_off=0, out=None, out_dtype=None, scale=None,
+                 flags=0, stream=None):
+    """q [B, Sq, >=Nh*128] bf16, k/v [B, Skv, >=Nkv*128] bf16 (views allowed: last dim contiguous)."""
+    import math
+
+    import torch
+    B, Sq = q.shape[0], q.shape[1]
+    Skv = k.shape[1]
+    if out is None:
+        out = torch.empty((B, Sq, Nh * 128), dtype=out_dtype or torch.bfloat16, device=q.device)
+    _check("acb_attn_prefill", lib().acb_attn_prefill(
+        _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0), v.stride(1),
+        _ptr(out), dtype_id(out), out.stride(0), out.stride(1), B, Sq, Skv, Nh, Nkv, 128, mask, window, causal_off,
+        scale if scale is not None else 1.0 / math.sqrt(128), flags, _stream(stream)))
     return out

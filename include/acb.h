@@ -153,6 +153,21 @@ ACB_API acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, in
                                  int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
                                  int flags, int * err_flag, acb_stream_t stream);
 
+/* Attention over whole sequences (flash tiling on bf16 tensor cores, fp32 softmax and
+ * accumulation), head_dim 128, GQA head h -> kv head h / (Nh/Nkv):
+ *   O[b,i,h] = softmax_j(Q[b,i,h].K[b,j,h'] * scale + mask) V[b,j,h']
+ * Q/K/V bf16 with element strides per batch (*_bs) and per token (*_ts); heads are contiguous
+ * 128-element runs within a token row (so Q, K and V may be column views of one fused QKV
+ * row). mask: 0 none, 1 causal (key j <= i + causal_off), 2 sliding window (|i - j| <= window).
+ * O is f32 or bf16. Replaces ggml_flash_attn_ext / qwen3_attn_f32 / dit_attn_f32 at prefill
+ * (src/qwen3-enc.h:186-199; src/dit-graph.h:218-231 self-attention with the sliding-window and
+ * padding masks of dit-sampler.h:253-282, and 339-352 cross-attention). */
+ACB_API acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs,
+                                    int64_t k_ts, const void * v, int64_t v_bs, int64_t v_ts, void * o, int o_type,
+                                    int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv, int Nh, int Nkv,
+                                    int head_dim, int mask, int window, int causal_off, float scale, int flags,
+                                    acb_stream_t stream);
+
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 
 enum {

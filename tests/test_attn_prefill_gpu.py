@@ -1,0 +1,75 @@
+"""GPU: prefill / DiT attention (acb_attn_prefill) against a plain PyTorch fp32 softmax attention on
+the same bf16 Q/K/V, and against the oracle's ggml-CPU attention. The kernel rounds the
+probabilities to bf16 for the P.V product and uses exp2, so the bar is the bf16 tier:
+cosine >= 0.9999 and max_rel <= 1e-2 per output."""
+import math
+
+import numpy as np
+import pytest
+
+import acb
+import oracle as O
+from helpers import cos_sim, max_rel
+
+pytestmark = pytest.mark.gpu
+
+
+def torch_ref(q, k, v, Nh, Nkv, mask, window, causal_off):
+    import torch
+    B, Sq, _ = q.shape
+    Skv = k.shape[1]
+    G = Nh // Nkv
+    qf = q.float().view(B, Sq, Nh, 128).permute(0, 2, 1, 3)
+    kf = k.float().view(B, Skv, Nkv, 128).permute(0, 2, 1, 3).repeat_interleave(G, dim=1)
+    vf = v.float().view(B, Skv, Nkv, 128).permute(0, 2, 1, 3).repeat_interleave(G, dim=1)
+    s = (qf @ kf.transpose(-1, -2)) / math.sqrt(128)
+    i = torch.arange(Sq, device=q.device)[:, None]
+    j = torch.arange(Skv, device=q.device)[None, :]
+    if mask == acb.MASK_CAUSAL:
+        s = s.masked_fill(~(j <= i + causal_off), float("-inf"))
+    elif mask == acb.MASK_WINDOW:
+        s = s.masked_fill(~((i - j).abs() <= window), float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return (p @ vf).permute(0, 2, 1, 3).reshape(B, Sq, Nh * 128)
+
+
+@pytest.mark.parametrize("B,Sq,Skv,Nh,Nkv,mask,window", [
+    (1, 256, 256, 16, 8, acb.MASK_CAUSAL, 0),       # text encoder (config 1)
+    (8, 750, 750, 16, 8, acb.MASK_WINDOW, 128),     # DiT self-attention, even layers
+    (8, 750, 750, 16, 8, acb.MASK_NONE, 0),         # DiT self-attention, odd layers
+    (8, 750, 512, 16, 8, acb.MASK_NONE, 0),         # DiT cross-attention
+    (2, 77, 33, 4, 2, acb.MASK_NONE, 0),            # ragged tails
+    (1, 100, 300, 16, 8, acb.MASK_CAUSAL, 200),     # prefill continuing a cache (causal offset)
+])
+def test_attn_prefill_matches_fp32(cuda, B, Sq, Skv, Nh, Nkv, mask, window):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(Sq + Skv + mask)
+    q = (torch.randn(B, Sq, Nh * 128, device=cuda, generator=g) * 1.5).bfloat16()
+    k = (torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g) * 1.5).bfloat16()
+    v = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g).bfloat16()
+    causal_off = 200 if (mask == acb.MASK_CAUSAL and Skv > Sq) else 0
+    o = acb.attn_prefill(q, k, v, Nh, Nkv, mask=mask, window=window, causal_off=causal_off, out_dtype=torch.float32)
+    ref = torch_ref(q, k, v, Nh, Nkv, mask, window, causal_off)
+    got, want = o.cpu().numpy(), ref.cpu().numpy()
+    for b in range(B):
+        c, r = cos_sim(got[b], want[b]), max_rel(got[b], want[b])
+        assert c >= 0.9999 and r <= 1e-2, (b, c, r)
+
+
+def test_attn_prefill_views_of_fused_qkv_and_oracle(cuda):
+    """Q, K, V as column views of one fused bf16 QKV row (the GEMM output layout), compared with
+    the oracle's ggml-CPU attention (f32 path of qwen3_attn_f32, causal mask)."""
+    import torch
+    Nh, Nkv, S = 16, 8, 200
+    qkvd = (Nh + 2 * Nkv) * 128
+    g = torch.Generator(device=cuda).manual_seed(9)
+    qkv = torch.randn(1, S, qkvd, device=cuda, generator=g).bfloat16()
+    q, k, v = qkv[:, :, :Nh * 128], qkv[:, :, Nh * 128:(Nh + Nkv) * 128], qkv[:, :, (Nh + Nkv) * 128:]
+    o = acb.attn_prefill(q, k, v, Nh, Nkv, mask=acb.MASK_CAUSAL, out_dtype=torch.float32)
+    qn = q.float().cpu().numpy().reshape(S, Nh, 128)
+    kn = k.float().cpu().numpy().reshape(S, Nkv, 128)
+    vn = v.float().cpu().numpy().reshape(S, Nkv, 128)
+    mask = np.where(np.arange(S)[None, :] <= np.arange(S)[:, None], 0.0, -np.inf).astype(np.float32)
+    ref = O.attention(qn, kn, vn, O.F32, mask, 1.0 / math.sqrt(128)).reshape(S, Nh * 128)
+    got = o[0].cpu().numpy()
+    assert cos_sim(got, ref) >= 0.9999 and max_rel(got, ref) <= 1e-2
