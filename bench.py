@@ -294,6 +294,12 @@ def run_ours(args):
     if args.workloads == "gemm":
         print(json.dumps(run_gemm_shapes(dev)), flush=True)
         return
+    if args.workloads == "enc":
+        r = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands (Q8_0-quantised activations)")),
+                  flush=True)
+        return
     if "ops" not in args.workloads.split(","):
         # LM-only run (profiling): one line with the decode result
         lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt, gen_len=args.lm_gen)
@@ -390,6 +396,10 @@ def run_ours(args):
         del wls, ops, evs
         torch.cuda.empty_cache()
         lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt, gen_len=args.lm_gen)
+    enc = None
+    if "enc" in args.workloads.split(",") and ws == 1:
+        torch.cuda.empty_cache()
+        enc = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
 
     if rank == 0:
         line = {"metric": "fused-op HBM GB/s (config 2 op-chain, algorithmic bytes)", "value": round(value, 2),
@@ -407,7 +417,8 @@ def run_ours(args):
                                              for k, v in per_op.items()},
                 "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-                "gpu_launches": n_launch, "clocks": clocks, "cpu_baseline": cpu, "lm_decode": lm}
+                "gpu_launches": n_launch, "clocks": clocks, "cpu_baseline": cpu, "lm_decode": lm,
+                "text_encoder": enc}
         print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()
@@ -593,6 +604,98 @@ def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None, prompt_len=L
     return res
 
 
+ENC_S = 256
+
+
+def enc_flops(cfg, S) -> int:
+    """Algorithmic FLOPs of one encoder forward: every linear (2*S*N*K) plus causal attention
+    (QK^T and PV over the S(S+1)/2 unmasked pairs, 2*D flops each, per head)."""
+    H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
+    Nh, Nkv, D = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    lin = (Nh + 2 * Nkv) * D * H + H * Nh * D + 2 * F * H + H * F
+    att = 2 * (2 * D) * Nh * (S * (S + 1) // 2)
+    return L * (2 * S * lin + att)
+
+
+def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
+    """Config 1 on this GPU: the Qwen3-0.6B-shaped text encoder, 256 tokens, Q8_0 weights."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+    import synthetic
+
+    cfg = dict(synthetic.QWEN3_EMBED_0_6B)
+    path = os.path.join(tempfile.gettempdir(), f"acb_bench_enc06_q8_0_r{rank}.gguf")
+    keep = {} if want_cpu else None
+    synthetic.write_lm_gguf(path, cfg, synthetic.policy_q8_0, seed=3, device=str(dev), keep=keep, prefix="",
+                            arch="qwen3")
+    enc = acb.Qwen3Encoder(path, device=dev.index or 0)
+    ids = np.random.default_rng(11).integers(0, cfg["vocab_size"], S).astype(np.int32)
+    d_ids = torch.from_numpy(ids).to(dev)
+    d_out = torch.empty((S, cfg["hidden_size"]), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(5):
+        enc.forward_device(d_ids, d_out, stream)
+    torch.cuda.synchronize()
+    # the 0.9 GB of f16 weights exceed the 126 MB L2: back-to-back forwards stream them from HBM
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        enc.forward_device(d_ids, d_out, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    fl = enc_flops(cfg, S)
+    # e2e: host ids in, host hidden states out (acb_qwen3_forward, the qwen3_forward drop-in)
+    out = enc.forward(ids)
+    t0 = time.perf_counter()
+    e2e_n = 20
+    for _ in range(e2e_n):
+        out = enc.forward(ids)
+    e2e_s = (time.perf_counter() - t0) / e2e_n
+    peaks, kind = measured_peaks()
+    res = {
+        "metric": "text-encoder forwards/s (config 1: Qwen3-0.6B shape, Q8_0 weights, 256 tokens)",
+        "value": round(1e3 / ms, 2), "unit": "forward/s", "higher_is_better": True, "ms_per_forward": round(ms, 4),
+        "tokens_per_s": round(S * 1e3 / ms, 1),
+        "config": {"workload": "config1_text_encoder_q8_0", "tokens": S, "layers": cfg["num_hidden_layers"],
+                   "weights": "Q8_0 in the GGUF, resident f16 copies; activations quantised like ggml (Q8_0)",
+                   "weight_bytes_device": enc.weight_bytes()},
+        "roofline": {"kernel": "whole forward (tcgen05 GEMMs dominate)", "bound": "tensor",
+                     "achieved": round(fl / (ms * 1e-3) / 1e12, 1), "peak": peaks["bf16_tflops"],
+                     "peak_kind": kind, "unit": "TFLOP/s",
+                     "frac": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+                     "flops_per_forward": fl, "traffic": None},
+        "e2e": {"value": round(1.0 / e2e_s, 2), "unit": "forward/s", "h2d_bytes_per_step": S * 4,
+                "d2h_bytes_per_step": S * cfg["hidden_size"] * 4, "path": "acb_qwen3_forward"},
+        "gpu_launches_per_forward": 2 + cfg["num_hidden_layers"] * 12,
+    }
+    if want_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        tensors = {n: (qt, raw, K, raw.shape[0] if raw.ndim > 1 else 1) for n, (qt, raw, K) in keep.items()}
+        om = O.qwen3_from_gguf_tensors(cfg, tensors, prefix="")
+        t0 = time.perf_counter()
+        ref = om.encode(ids)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": round(1.0 / dt, 4), "unit": "forward/s", "cores": O.get_threads(),
+                               "kind": "port", "sample": "one full oracle forward (ggml-CPU mul_mat semantics), "
+                                                         "same weights and ids"}
+        num = (out.astype(np.float64) * ref).sum(1)
+        den = np.linalg.norm(out, axis=1) * np.linalg.norm(ref, axis=1)
+        res["parity_vs_oracle"] = {"min_row_cosine": round(float((num / den).min()), 8)}
+    enc.close()
+    del keep
+    try:
+        os.remove(path)
+    except OSError:
+        pass
+    return res
+
+
 def cpu_lm_sample(cfg, keep, prompt, n_prefill=8, n_decode=3):
     """Oracle decode of the same weights on the host cores (bounded sample: a short prefill,
     then n_decode timed one-token steps; each step streams every weight like the GPU step)."""
@@ -625,9 +728,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
-    ap.add_argument("--workloads", default="ops,lm",
-                    help="comma list: ops (config 2, the headline line), lm (config 3 decode, N=1); "
-                         "or `gemv` alone for the per-shape GEMV microbench")
+    ap.add_argument("--workloads", default="ops,lm,enc",
+                    help="comma list: ops (config 2, the headline line), lm (config 3 decode, N=1), "
+                         "enc (config 1 text encoder, N=1); or `gemv` / `gemm` / `enc` alone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -93,6 +93,15 @@ def lib():
             "acb_qw3lm_weight_bytes": (C.c_size_t, [P]),
             "acb_qw3lm_generate_greedy": (I, [P, P, I, I, I, P, P, P]),
             "acb_qw3lm_free": (None, [P]),
+            "acb_qwen3_load_text_encoder": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
+            "acb_qwen3_weight_bytes": (C.c_size_t, [P]),
+            "acb_qwen3_forward": (I, [P, P, I, P]),
+            "acb_qwen3_forward_device": (I, [P, P, I, P, P]),
+            "acb_qwen3_embed_lookup": (I, [P, P, I, P]),
+            "acb_qwen3_free": (None, [P]),
+            "acb_act_quant": (I, [P, I64, I64, I64, I, P, I, I64, P]),
+            "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
+            "acb_vec_dot_type": (I, [I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -218,6 +227,7 @@ def get_rows(table, table_type, n_rows, cols, ids, out=None, out_dtype=None, err
 PRO_X, PRO_RMSNORM, PRO_SUM_SPLITS, PRO_SWIGLU = 0, 1, 2, 3
 EPI_STORE, EPI_ADD = 0, 1
 FLAG_PDL = 1
+FLAG_F16 = 2  # tensor-core operands are f16 (acb_gemm_bf16, acb_attn_prefill)
 
 
 def gemv(W, w_type, N, K, x, M=None, prologue=PRO_X, x_stride=None, norm_w=None, eps=1e-6, n_split=1, y=None,
@@ -351,8 +361,11 @@ class QW3LM:
 
 def gemm_bf16(A, B, out=None, out_dtype=None, bias=None, res=None, gate=None, rows_per_sample=None, flags=0,
               err=None, stream=None):
-    """C = A @ B.T (+ bias) (res + C or res + C * gate) on tcgen05. A [M,K], B [N,K] bf16 CUDA tensors."""
+    """C = A @ B.T (+ bias) (res + C or res + C * gate) on tcgen05. A [M,K], B [N,K] bf16 (or f16,
+    which sets FLAG_F16) CUDA tensors."""
     import torch
+    if A.dtype == torch.float16:
+        flags |= FLAG_F16
     M, K = A.shape
     N = B.shape[0]
     if out is None:
@@ -370,10 +383,13 @@ MASK_NONE, MASK_CAUSAL, MASK_WINDOW = 0, 1, 2
 
 def attn_prefill(q, k, v, Nh, Nkv, mask=MASK_NONE, window=0, causal_off=0, out=None, out_dtype=None, scale=None,
                  flags=0, stream=None):
-    """q [B, Sq, >=Nh*128] bf16, k/v [B, Skv, >=Nkv*128] bf16 (views allowed: last dim contiguous)."""
+    """q [B, Sq, >=Nh*128] bf16 (or f16, which sets FLAG_F16), k/v [B, Skv, >=Nkv*128] of the same
+    type (views allowed: last dim contiguous)."""
     import math
 
     import torch
+    if q.dtype == torch.float16:
+        flags |= FLAG_F16
     B, Sq = q.shape[0], q.shape[1]
     Skv = k.shape[1]
     if out is None:
@@ -383,3 +399,86 @@ def attn_prefill(q, k, v, Nh, Nkv, mask=MASK_NONE, window=0, causal_off=0, out=N
         _ptr(out), dtype_id(out), out.stride(0), out.stride(1), B, Sq, Skv, Nh, Nkv, 128, mask, window, causal_off,
         scale if scale is not None else 1.0 / math.sqrt(128), flags, _stream(stream)))
     return out
+
+
+def vec_dot_type(weight_type: int) -> int:
+    return lib().acb_vec_dot_type(weight_type)
+
+
+def act_quant(x, vec_type, out=None, stream=None):
+    """x [M, K] f32 CUDA -> [M, K] f16 (bf16 for vec_type BF16) dequantised ggml activation."""
+    import torch
+    M, K = x.shape
+    dt = torch.bfloat16 if vec_type == BF16 else torch.float16
+    if out is None:
+        out = torch.empty((M, K), dtype=dt, device=x.device)
+    _check("acb_act_quant", lib().acb_act_quant(_ptr(x), x.stride(0), M, K, vec_type, _ptr(out), dtype_id(out),
+                                                out.stride(0), _stream(stream)))
+    return out
+
+
+def act_quant_swiglu(gu, F, vec_type, out=None, stream=None):
+    """gu [M, 2F] f32 fused gate|up rows -> act_quant(silu(g) * u) [M, F]."""
+    import torch
+    M = gu.shape[0]
+    dt = torch.bfloat16 if vec_type == BF16 else torch.float16
+    if out is None:
+        out = torch.empty((M, F), dtype=dt, device=gu.device)
+    _check("acb_act_quant_swiglu", lib().acb_act_quant_swiglu(
+        _ptr(gu), gu.stride(0), F, M, F, vec_type, _ptr(out), dtype_id(out), out.stride(0), _stream(stream)))
+    return out
+
+
+class Qwen3Encoder:
+    """Qwen3 encoder stack (acb_models.h): qwen3_load_text_encoder / qwen3_forward /
+    qwen3_embed_lookup of src/qwen3-enc.h."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        import numpy as np
+        self.np = np
+        h = C.c_void_p()
+        st = lib().acb_qwen3_load_text_encoder(gguf_path.encode(), device, C.byref(h))
+        if st != 0:
+            raise AcbError(f"acb_qwen3_load_text_encoder ({lib().acb_last_error().decode()})", st)
+        self.h = h
+        fields = ["hidden_size", "intermediate_size", "n_heads", "n_kv_heads", "head_dim", "n_layers",
+                  "rope_theta", "rms_norm_eps", "is_causal", "vocab_size"]
+
+        class Cfg(C.Structure):
+            _fields_ = [(f, C.c_float if f in ("rope_theta", "rms_norm_eps") else C.c_int) for f in fields]
+        c = Cfg()
+        fn = lib().acb_qwen3_get_config
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.POINTER(Cfg)]
+        _check("acb_qwen3_get_config", fn(self.h, C.byref(c)))
+        self.cfg = {f: getattr(c, f) for f in fields}
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().acb_qwen3_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def weight_bytes(self) -> int:
+        return lib().acb_qwen3_weight_bytes(self.h)
+
+    def forward(self, ids):
+        """Host ids [S] -> host hidden states [S][H] f32 (final RMSNorm applied)."""
+        ids = self.np.ascontiguousarray(ids, dtype=self.np.int32)
+        out = self.np.empty((ids.size, self.cfg["hidden_size"]), dtype=self.np.float32)
+        _check("acb_qwen3_forward", lib().acb_qwen3_forward(self.h, ids.ctypes.data, ids.size, out.ctypes.data))
+        return out
+
+    def forward_device(self, ids, out, stream=None):
+        """Device int32 ids [S] -> device f32 out [S][H], enqueued on the stream."""
+        _check("acb_qwen3_forward_device", lib().acb_qwen3_forward_device(
+            self.h, _ptr(ids), ids.numel(), _ptr(out), _stream(stream)))
+        return out
+
+    def embed_lookup(self, ids):
+        ids = self.np.ascontiguousarray(ids, dtype=self.np.int32)
+        out = self.np.empty((ids.size, self.cfg["hidden_size"]), dtype=self.np.float32)
+        _check("acb_qwen3_embed_lookup", lib().acb_qwen3_embed_lookup(self.h, ids.ctypes.data, ids.size,
+                                                                      out.ctypes.data))
+        return out

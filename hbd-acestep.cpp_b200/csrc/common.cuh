@@ -103,6 +103,13 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // ggml_rms_norm scale: sum of float squares accumulated in double, mean rounded to float,
 // 1/sqrt in IEEE float (the division and sqrt are correctly rounded under -prec-div/-prec-sqrt).
+// ggml_swiglu element: silu(g) * u with silu(g) = g / (1 + exp(-g)), IEEE division, each node
+// rounded once (every SwiGLU in the library uses this one definition).
+__device__ __forceinline__ float silu_times(float g, float u) {
+    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    return __fmul_rn(s, u);
+}
+
 __device__ __forceinline__ float rms_scale(double sumsq, int n, float eps) {
     float mean = (float) (sumsq / (double) n);
     return 1.0f / sqrtf(__fadd_rn(mean, eps));

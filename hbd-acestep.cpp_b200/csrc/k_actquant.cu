@@ -1,0 +1,218 @@
+// k_actquant.cu -- activation operand of the tensor-core linears with ggml-CPU's quantised
+// mul_mat arithmetic (the from_float step of ggml_mul_mat for Q8_0 / Q4_K / Q6_K / F16 / BF16
+// weights, reached from src/qwen3-enc.h:86-88 and src/dit-graph.h:36-49).
+//
+// One warp per 256-element chunk of a row; lane l holds elements [8l, 8l+8) in registers
+// (two 16-byte loads). Q8_0 blocks of 32 are four consecutive lanes (two xor shuffles for the
+// block max); a Q8_K block of 256 is the whole warp (five shuffles carrying value and index,
+// so the first element of largest magnitude wins as in the sequential reference). The
+// dequantised values d*q are written as f16 with one 16-byte store per lane. The SwiGLU variant
+// computes silu(g)*u from fused [gate | up] rows first (ggml_swiglu followed by the down
+// projection's quantisation, src/qwen3-enc.h:217-223, src/dit-graph.h:259-268).
+#include "common.cuh"
+
+namespace acb {
+
+constexpr int kAqWarps = 8;
+
+__device__ __forceinline__ void load8(const float * p, bool vec, float * v) {
+    if (vec) {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        const float4 b = *reinterpret_cast<const float4 *>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            v[e] = p[e];
+        }
+    }
+}
+
+template <int VT, bool SWIGLU>
+__global__ void __launch_bounds__(kAqWarps * 32)
+    act_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t up_off, int64_t rows, int64_t K,
+                     void * __restrict__ y, int64_t ys, bool vec_in, bool vec_out) {
+    const int     lane   = threadIdx.x & 31;
+    const int64_t chunks = (K + 255) / 256;
+    const int64_t item   = (int64_t) blockIdx.x * kAqWarps + (threadIdx.x >> 5);
+    if (item >= rows * chunks) {
+        return;
+    }
+    const int64_t r     = item / chunks;
+    const int64_t c0    = (item - r * chunks) * 256 + lane * 8;
+    const bool    valid = c0 < K;  // K is a multiple of 32: a lane is all in or all out
+    const float * xr    = x + r * xs + c0;
+    float         v[8];
+    if (valid) {
+        load8(xr, vec_in, v);
+        if (SWIGLU) {
+            float u[8];
+            load8(xr + up_off, vec_in, u);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                v[e] = silu_times(v[e], u[e]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            v[e] = 0.0f;
+        }
+    }
+
+    float o[8];
+    if (VT == ACB_TYPE_Q8_0) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            amax = fmaxf(amax, fabsf(v[e]));
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        const float d  = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        const float dh = __half2float(__float2half_rn(d));  // the block stores d as f16
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            o[e] = __fmul_rn(dh, roundf(__fmul_rn(v[e], id)));
+        }
+    } else if (VT == ACB_TYPE_Q8_K) {
+        float amax = 0.0f, mx = 0.0f;
+        int   idx  = 0x7fffffff;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float a = fabsf(v[e]);
+            if (a > amax) {  // first index of the largest magnitude within the lane
+                amax = a;
+                mx   = v[e];
+                idx  = lane * 8 + e;
+            }
+        }
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, s);
+            const float om = __shfl_xor_sync(0xffffffffu, mx, s);
+            const int   oi = __shfl_xor_sync(0xffffffffu, idx, s);
+            if (oa > amax || (oa == amax && oi < idx)) {
+                amax = oa;
+                mx   = om;
+                idx  = oi;
+            }
+        }
+        if (amax == 0.0f) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                o[e] = 0.0f;
+            }
+        } else {
+            const float iscale = __fdiv_rn(-127.0f, mx);
+            const float d      = __fdiv_rn(1.0f, iscale);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                int q = __float2int_rn(__fmul_rn(iscale, v[e]));
+                q     = q < 127 ? q : 127;
+                o[e]  = __fmul_rn(d, (float) q);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            o[e] = v[e];
+        }
+    }
+    if (!valid) {
+        return;
+    }
+    using et = typename io<VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16>::t;
+    constexpr int OT = VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
+    et * yr = reinterpret_cast<et *>(y) + r * ys + c0;
+    if (vec_out) {
+        vec16<OT> pk;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            pk.v[e] = io<OT>::from_f(o[e]);
+        }
+        *reinterpret_cast<uint4 *>(yr) = pk.u;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            yr[e] = io<OT>::from_f(o[e]);
+        }
+    }
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" int acb_vec_dot_type(int weight_type) {
+    switch (weight_type) {
+        case ACB_TYPE_Q8_0:
+            return ACB_TYPE_Q8_0;
+        case ACB_TYPE_Q4_K:
+        case ACB_TYPE_Q6_K:
+            return ACB_TYPE_Q8_K;
+        case ACB_TYPE_F16:
+            return ACB_TYPE_F16;
+        case ACB_TYPE_BF16:
+            return ACB_TYPE_BF16;
+        default:
+            return -1;
+    }
+}
+
+template <bool SWIGLU>
+static acb_status launch_act_quant(const float * x, int64_t x_stride, int64_t up_off, int64_t rows, int64_t K,
+                                   int vec_type, void * y, int y_type, int64_t y_stride, cudaStream_t st) {
+    const int want_y = vec_type == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
+    if (y_type != want_y || K % 32 != 0 || (vec_type == ACB_TYPE_Q8_K && K % 256 != 0)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (rows == 0) {
+        return ACB_OK;
+    }
+    const bool vin = (x_stride % 4 == 0) && (up_off % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    const bool vout = (y_stride % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    const int64_t items = rows * ((K + 255) / 256);
+    const dim3    grid((unsigned) ((items + kAqWarps - 1) / kAqWarps));
+#define ACB_AQ(VT)                                                                                              \
+    act_quant_kernel<VT, SWIGLU><<<grid, kAqWarps * 32, 0, st>>>(x, x_stride, up_off, rows, K, y, y_stride, vin, \
+                                                                 vout)
+    switch (vec_type) {
+        case ACB_TYPE_Q8_0:
+            ACB_AQ(ACB_TYPE_Q8_0);
+            break;
+        case ACB_TYPE_Q8_K:
+            ACB_AQ(ACB_TYPE_Q8_K);
+            break;
+        case ACB_TYPE_F16:
+            ACB_AQ(ACB_TYPE_F16);
+            break;
+        case ACB_TYPE_BF16:
+            ACB_AQ(ACB_TYPE_BF16);
+            break;
+        default:
+            return ACB_ERR_UNSUPPORTED;
+    }
+#undef ACB_AQ
+    return launch_status();
+}
+
+extern "C" acb_status acb_act_quant(const float * x, int64_t x_stride, int64_t rows, int64_t K, int vec_type, void * y,
+                                    int y_type, int64_t y_stride, acb_stream_t stream) {
+    if (!x || !y || rows < 0 || K <= 0 || x_stride < K || y_stride < K) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    return launch_act_quant<false>(x, x_stride, 0, rows, K, vec_type, y, y_type, y_stride, (cudaStream_t) stream);
+}
+
+extern "C" acb_status acb_act_quant_swiglu(const float * gu, int64_t gu_stride, int64_t up_offset, int64_t rows,
+                                           int64_t F, int vec_type, void * y, int y_type, int64_t y_stride,
+                                           acb_stream_t stream) {
+    if (!gu || !y || rows < 0 || F <= 0 || up_offset < F || gu_stride < up_offset + F || y_stride < F) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    return launch_act_quant<true>(gu, gu_stride, up_offset, rows, F, vec_type, y, y_type, y_stride,
+                                  (cudaStream_t) stream);
+}

@@ -2,7 +2,7 @@
 // src/qwen3-enc.h:186-199) and the DiT (self-attention with the even layers' sliding window,
 // cross-attention to the condition; src/dit-graph.h:218-231, 339-352):
 //     O[b,i,h,:] = softmax_j( Q[b,i,h,:] . K[b,j,h/G,:] * scale + mask(i,j) ) V[b,j,h/G,:]
-// Flash-attention tiling with bf16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation):
+// Flash-attention tiling with bf16 or f16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation):
 // a CTA owns 64 queries of one (batch, head); four warps own 16 query rows each with their Q
 // fragments in registers; 64-key K/V blocks stream through a cp.async double buffer (rows padded
 // to 272 bytes so ldmatrix is conflict-free); the softmax is online in fp32 (exp2 with the scale
@@ -63,15 +63,28 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t & r0, uint32_t & r1, uint32_t
                  : "r"(ptx::smem_u32(p)));
 }
 
-__device__ __forceinline__ void mma_bf16(float * c, const uint32_t * a, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+// m16n8k16 with fp32 accumulation; A and B both bf16, or both f16
+template <bool F16> __device__ __forceinline__ void mma16(float * c, const uint32_t * a, uint32_t b0, uint32_t b1) {
+    if (F16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+template <bool F16> __device__ __forceinline__ uint32_t pack16(float lo, float hi) {
+    if (F16) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&h);
 }
@@ -86,7 +99,7 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16 * sm, const __nv_bfloat1
     }
 }
 
-template <int MASK>
+template <int MASK, bool F16>
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     __nv_bfloat16 * sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
@@ -168,8 +181,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
                 const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
                 const int d   = ks * 16 + ((lane >> 3) & 1) * 8;
                 ldsm_x4(b0, b1, b2, b3, Kb + key * kAttnPad + d);
-                mma_bf16(s[2 * np], qf[ks], b0, b1);
-                mma_bf16(s[2 * np + 1], qf[ks], b2, b3);
+                mma16<F16>(s[2 * np], qf[ks], b0, b1);
+                mma16<F16>(s[2 * np + 1], qf[ks], b2, b3);
             }
         }
         // scale (in log2 units), mask, online softmax
@@ -214,8 +227,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
                 rs[e >> 1] += p[e];
             }
             // C-fragment (rows r, r+8; cols 2c, 2c+1) -> A-fragment halves of key step n/2
-            pf[n >> 1][(n & 1) * 2 + 0] = pack_bf16(p[0], p[1]);
-            pf[n >> 1][(n & 1) * 2 + 1] = pack_bf16(p[2], p[3]);
+            pf[n >> 1][(n & 1) * 2 + 0] = pack16<F16>(p[0], p[1]);
+            pf[n >> 1][(n & 1) * 2 + 1] = pack16<F16>(p[2], p[3]);
         }
 #pragma unroll
         for (int r = 0; r < 2; r++) {
@@ -242,8 +255,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
                 const int key = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
                 const int d   = np * 16 + (lane >> 4) * 8;
                 ldsm_x4_t(b0, b1, b2, b3, Vb + key * kAttnPad + d);
-                mma_bf16(o[2 * np], af, b0, b1);
-                mma_bf16(o[2 * np + 1], af, b2, b3);
+                mma16<F16>(o[2 * np], af, b0, b1);
+                mma16<F16>(o[2 * np + 1], af, b2, b3);
             }
         }
         __syncthreads();
@@ -266,9 +279,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
             if (a.o_type == ACB_TYPE_F32) {
                 float * dst = reinterpret_cast<float *>(a.o) + base + d;
                 *reinterpret_cast<float2 *>(dst) = make_float2(v0, v1);
-            } else {
+            } else if (a.o_type == ACB_TYPE_BF16) {
                 __nv_bfloat16 * dst = reinterpret_cast<__nv_bfloat16 *>(a.o) + base + d;
                 *reinterpret_cast<__nv_bfloat162 *>(dst) = __floats2bfloat162_rn(v0, v1);
+            } else {
+                __half * dst = reinterpret_cast<__half *>(a.o) + base + d;
+                *reinterpret_cast<__half2 *>(dst) = __floats2half2_rn(v0, v1);
             }
         }
     }
@@ -287,7 +303,8 @@ extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_t
     if (!q || !k || !v || !o || batch <= 0 || Sq <= 0 || Skv <= 0 || Nh <= 0 || Nkv <= 0 || Nh % Nkv != 0) {
         return ACB_ERR_INVALID_ARG;
     }
-    if (head_dim != kAttnD || (o_type != ACB_TYPE_F32 && o_type != ACB_TYPE_BF16) || mask < 0 || mask > 2) {
+    if (head_dim != kAttnD || (o_type != ACB_TYPE_F32 && o_type != ACB_TYPE_BF16 && o_type != ACB_TYPE_F16) ||
+        mask < 0 || mask > 2) {
         return ACB_ERR_UNSUPPORTED;
     }
     if ((q_ts | k_ts | v_ts | q_bs | k_bs | v_bs) % 8 != 0 || reinterpret_cast<uintptr_t>(q) % 16 ||
@@ -328,9 +345,11 @@ extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_t
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = (flags & 1) ? attr : nullptr;
     cfg.numAttrs                                       = (flags & 1) ? 1 : 0;
-    void (*kern)(const AttnArgs) = mask == MASK_CAUSAL ? attn_prefill_kernel<MASK_CAUSAL>
-                                   : mask == MASK_WINDOW ? attn_prefill_kernel<MASK_WINDOW>
-                                                         : attn_prefill_kernel<MASK_NONE>;
+    const bool f16 = (flags & ACB_FLAG_F16) != 0;
+    void (*kern)(const AttnArgs) =
+        mask == MASK_CAUSAL ? (f16 ? attn_prefill_kernel<MASK_CAUSAL, true> : attn_prefill_kernel<MASK_CAUSAL, false>)
+        : mask == MASK_WINDOW ? (f16 ? attn_prefill_kernel<MASK_WINDOW, true> : attn_prefill_kernel<MASK_WINDOW, false>)
+                              : (f16 ? attn_prefill_kernel<MASK_NONE, true> : attn_prefill_kernel<MASK_NONE, false>);
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) {

@@ -9,8 +9,7 @@
 namespace acb {
 
 template <int T> __device__ __forceinline__ float silu_mul(float g, float u) {
-    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-    return __fmul_rn(s, u);
+    return silu_times(g, u);
 }
 
 template <int TI, int TO, int U>

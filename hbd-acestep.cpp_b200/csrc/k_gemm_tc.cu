@@ -1,15 +1,15 @@
 // k_gemm_tc.cu -- tensor-core GEMM for the dense prefill / DiT linears (src/dit-graph.h:36-49 and
 // every ggml_mul_mat of dit_ggml_build_layer at M = tokens):
-//     C[m][n] = epilogue( sum_k A[m][k] * B[n][k] ),  A, B bf16 K-major, fp32 accumulation.
+//     C[m][n] = epilogue( sum_k A[m][k] * B[n][k] ),  A, B bf16 or f16 K-major, fp32 accumulation.
 //
 // sm_100a design (one persistent CTA per SM, 6 warps, no clusters, no multicast):
 //   warp 0      TMA producer: A tile 128x64 and B tile 256x64 per stage (128-byte swizzle) into a
 //               4-stage ring (48 KB per stage), completion on an mbarrier per stage;
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators), one elected thread
-//               issues tcgen05.mma (M=128, N=256, K=16; kind::f16 with bf16 inputs) and releases
+//               issues tcgen05.mma (M=128, N=256, K=16; kind::f16 with bf16 or f16 inputs) and releases
 //               ring stages / publishes finished accumulators with tcgen05.commit;
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quarter, fused
-//               bias / residual / DiT gated residual, bf16 or f32 stores; the accumulator is
+//               bias / residual / DiT gated residual, f32, bf16 or f16 stores; the accumulator is
 //               handed back so the MMA of the next tile overlaps this epilogue.
 // Every mbarrier wait is bounded; on a timeout the kernel records ACB_DEVERR_TIMEOUT, stops, and
 // still frees its TMEM.
@@ -34,7 +34,7 @@ enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RES = 2, EPI_GATED_RES = 4 };
 struct GemmArgs {
     int64_t       M, N, K;
     void *        C;
-    int           c_type;  // ACB_TYPE_F32 or ACB_TYPE_BF16
+    int           c_type;  // ACB_TYPE_F32, ACB_TYPE_BF16 or ACB_TYPE_F16
     int64_t       ldc;
     const float * bias;    // [N] or null
     int           epi;     // bit set of EPI_*
@@ -65,12 +65,14 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return (uint64_t) ((saddr & 0x3FFFF) >> 4) | ((uint64_t) (1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, M=128, N=256.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (M >> 4) << 24);
+// kind::f16 instruction descriptor: fp32 accumulate (bits 4-5 = 1), A and B both bf16 (bits
+// 7-9 and 10-12 = 1) or both f16 (0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_kind_f16(int M, int N, bool f16) {
+    return (1u << 4) | (f16 ? 0u : ((1u << 7) | (1u << 10))) | ((uint32_t) (N >> 3) << 17) |
+           ((uint32_t) (M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void umma_f16kind(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
@@ -109,9 +111,32 @@ __device__ __forceinline__ void flag_timeout(int * err) {
     }
 }
 
+// 32 accumulator columns of one row to a 16-bit C (vector stores when whole and aligned)
+template <int T>
+__device__ __forceinline__ void store_row16(void * C, int64_t off, const float * v, bool full_cols, int left) {
+    using et = typename io<T>::t;
+    et * dst = reinterpret_cast<et *>(C) + off;
+    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            vec16<T> pk;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                pk.v[e] = io<T>::from_f(v[j + e]);
+            }
+            *reinterpret_cast<uint4 *>(dst + j) = pk.u;
+        }
+    } else {
+        for (int j = 0; j < 32 && j < left; j++) {
+            dst[j] = io<T>::from_f(v[j]);
+        }
+    }
+}
+
 // ---- the kernel ------------------------------------------------------------------------------------
+template <bool F16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs g) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -175,7 +200,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16(kBM, kBN);
+            constexpr uint32_t idesc = idesc_kind_f16(kBM, kBN, F16);
             int                it    = 0;
             int                tile  = 0;
             for (int64_t w = blockIdx.x; w < n_work && !abort_flag; w += gridDim.x, tile++) {
@@ -199,7 +224,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t b0 = a0 + kATile;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; kk++) {
-                        umma_bf16(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                        umma_f16kind(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
                                   (kt | kk) != 0 ? 1u : 0u);
                     }
                     umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
@@ -268,26 +293,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             dst[j] = v[j];
                         }
                     }
+                } else if (g.c_type == ACB_TYPE_BF16) {
+                    store_row16<ACB_TYPE_BF16>(g.C, m * g.ldc + nc, v, full_cols, (int) (g.N - nc));
                 } else {
-                    __nv_bfloat16 * dst = reinterpret_cast<__nv_bfloat16 *>(g.C) + m * g.ldc + nc;
-                    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 8) {
-                            union {
-                                __nv_bfloat16 h[8];
-                                uint4         u;
-                            } pk;
-#pragma unroll
-                            for (int e = 0; e < 8; e++) {
-                                pk.h[e] = __float2bfloat16_rn(v[j + e]);
-                            }
-                            *reinterpret_cast<uint4 *>(dst + j) = pk.u;
-                        }
-                    } else {
-                        for (int j = 0; j < 32 && nc + j < g.N; j++) {
-                            dst[j] = __float2bfloat16_rn(v[j]);
-                        }
-                    }
+                    store_row16<ACB_TYPE_F16>(g.C, m * g.ldc + nc, v, full_cols, (int) (g.N - nc));
                 }
                 }  // valid row and column chunk
             }
@@ -326,8 +335,9 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// bf16 row-major [rows][ld] (K contiguous), box = box_rows x 64 elements, 128-byte swizzle
-static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+// 16-bit row-major [rows][ld] (K contiguous), box = box_rows x 64 elements, 128-byte swizzle
+static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K, int64_t ld, int box_rows,
+                     bool f16) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) {
         return false;
@@ -336,7 +346,7 @@ static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K
     const cuuint64_t strides[1] = { (cuuint64_t) (ld * 2) };
     const cuuint32_t box[2]     = { (cuuint32_t) kBK, (cuuint32_t) box_rows };
     const cuuint32_t estr[2]    = { 1, 1 };
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+    return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -356,7 +366,7 @@ extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B,
         reinterpret_cast<uintptr_t>(B) % 16 != 0) {
         return ACB_ERR_UNSUPPORTED;
     }
-    if (c_type != ACB_TYPE_F32 && c_type != ACB_TYPE_BF16) {
+    if (c_type != ACB_TYPE_F32 && c_type != ACB_TYPE_BF16 && c_type != ACB_TYPE_F16) {
         return ACB_ERR_UNSUPPORTED;
     }
     if (gate && (!res || rows_per_sample <= 0)) {
@@ -378,13 +388,16 @@ extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B,
     g.rows_per_sample = rows_per_sample > 0 ? rows_per_sample : 1;
     g.err             = err_flag;
     CUtensorMap ta, tb;
-    if (!make_map(&ta, A, M, K, lda, kBM) || !make_map(&tb, B, N, K, ldb, kBN)) {
+    const bool f16 = (flags & ACB_FLAG_F16) != 0;
+    if (!make_map(&ta, A, M, K, lda, kBM, f16) || !make_map(&tb, B, N, K, ldb, kBN, f16)) {
         return ACB_ERR_CUDA;
     }
     const int64_t work = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
     const int     grid = (int) (work < num_sms() ? work : num_sms());
     const size_t  smem = (size_t) kStages * kStageBytes + 1024 + 256;
-    cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
+        f16 ? gemm_tc_kernel<true> : gemm_tc_kernel<false>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim            = dim3((unsigned) grid);
     cfg.blockDim           = dim3(kGemmThreads);
@@ -395,7 +408,7 @@ extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = (flags & 1) ? attr : nullptr;
     cfg.numAttrs                                       = (flags & 1) ? 1 : 0;
-    const cudaError_t e                                = cudaLaunchKernelEx(&cfg, gemm_bf16_tc_kernel, ta, tb, g);
+    const cudaError_t e                                = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
     if (e != cudaSuccess) {
         set_last_cuda_error(e);
         return ACB_ERR_CUDA;

@@ -1,0 +1,479 @@
+// qwen3_enc.cpp -- the Qwen3 encoder stack of acestep.cpp (src/qwen3-enc.h) on libacb kernels.
+//
+// Prefill over a whole prompt is GEMM-shaped, so every linear runs on the tcgen05 tensor-core
+// GEMM over resident f16 copies of the weights (dequantised exactly from their GGUF blocks at
+// load, then rounded to f16), with the activation quantised the way ggml's quantised mul_mat
+// does it (acb_act_quant), so the products are the reference's up to f16 rounding. One forward
+// for S tokens, per layer:
+//   RMSNorm * input_layernorm                h (f32)       -> xn (f32)
+//   activation quantisation                  xn            -> xq (f16)
+//   GEMM  Q||K||V                            xq            -> qkv (f16 [S][(Nh+2Nkv)D])
+//   q/k RMSNorm + NeoX RoPE (2 launches)     qkv columns   -> q, k (f16, head-contiguous)
+//   flash attention, causal                  q, k, v = qkv column view -> att (f32)
+//   activation quantisation                  att           -> xq
+//   GEMM  o_proj, epilogue + h               xq            -> h (in place)
+//   RMSNorm * post_attention_layernorm       h             -> xn
+//   activation quantisation                  xn            -> xq
+//   GEMM  gate||up                           xq            -> gu (f32 [S][2F])
+//   SwiGLU + activation quantisation         gu            -> xq [S][F]
+//   GEMM  down_proj, epilogue + h            xq            -> h (in place)
+// then the final RMSNorm into f32 output. The chain for each S is captured once as a CUDA
+// graph (tensor-core launches with programmatic dependent launch) and replayed.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/acb_models.h"
+#include "gguf.h"
+#include "host_common.h"
+#include "weights.h"
+
+using namespace acb;
+
+namespace {
+
+// One tensor-core linear: resident 16-bit weight rows, the activation format it expects and the
+// GEMM operand flag.
+struct Lin {
+    uint16_t * w   = nullptr;  // [N][K] f16 (bf16 for BF16 weights)
+    int        vec = -1;       // ggml vec-dot type of the source weights
+    int        op  = 0;        // ACB_FLAG_F16 or 0 (bf16 operands)
+    int        N = 0, K = 0;
+
+    int act_type() const { return op ? ACB_TYPE_F16 : ACB_TYPE_BF16; }
+};
+
+struct EncLayer {
+    DevTensor *attn_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    Lin        qkv, o, gu, down;
+};
+
+constexpr int kPdl = ACB_FLAG_PDL;
+
+}  // namespace
+
+struct acb_qwen3_enc {
+    int                   device = 0;
+    acb_qwen3_config      c{};
+    WeightArena           arena;  // embedding table (GGUF type) and F32 norms
+    DevBuf                w16;    // every linear, 16-bit
+    DevTensor *           embed = nullptr, *final_norm = nullptr;
+    std::vector<EncLayer> layers;
+    cudaStream_t          st = nullptr;
+
+    // scratch for up to cap tokens
+    int                            cap = 0;
+    DevBuf                         ids, pos, rope, h, xn, xq, qkv, q, k, att, gu, out, err;
+    std::map<int, cudaGraphExec_t> graphs;  // one per S
+
+    ~acb_qwen3_enc() {
+        cudaSetDevice(device);
+        drop_graphs();
+        if (st) {
+            cudaStreamDestroy(st);
+        }
+    }
+
+    void drop_graphs() {
+        for (auto & kv : graphs) {
+            cudaGraphExecDestroy(kv.second);
+        }
+        graphs.clear();
+    }
+
+    int nqkv() const { return (c.n_heads + 2 * c.n_kv_heads) * c.head_dim; }
+
+    acb_status reserve(int S);
+    acb_status linear(const Lin & L, const float * x, int64_t xs, int S, void * C, int c_type, int64_t ldc,
+                      const float * res, cudaStream_t s);
+    acb_status enqueue(int S, cudaStream_t s);
+    acb_status run(int S, cudaStream_t s);
+};
+
+acb_status acb_qwen3_enc::reserve(int S) {
+    if (S <= cap) {
+        return ACB_OK;
+    }
+    drop_graphs();
+    const int    n  = std::max(S, 256);
+    const size_t H  = (size_t) c.hidden_size, F = (size_t) c.intermediate_size;
+    const size_t QD = (size_t) c.n_heads * c.head_dim, KD = (size_t) c.n_kv_heads * c.head_dim;
+    const size_t XQ = std::max({ H, QD, F });
+    bool         bad = false;
+    bad |= ids.alloc((size_t) n * 4) != ACB_OK;
+    bad |= pos.alloc((size_t) n * 4, false) != ACB_OK;
+    bad |= h.alloc((size_t) n * H * 4) != ACB_OK;
+    bad |= xn.alloc((size_t) n * H * 4) != ACB_OK;
+    bad |= xq.alloc((size_t) n * XQ * 2) != ACB_OK;
+    bad |= qkv.alloc((size_t) n * nqkv() * 2) != ACB_OK;
+    bad |= q.alloc((size_t) n * QD * 2) != ACB_OK;
+    bad |= k.alloc((size_t) n * KD * 2) != ACB_OK;
+    bad |= att.alloc((size_t) n * QD * 4) != ACB_OK;
+    bad |= gu.alloc((size_t) n * 2 * F * 4) != ACB_OK;
+    bad |= out.alloc((size_t) n * H * 4) != ACB_OK;
+    bad |= rope.alloc((size_t) n * c.head_dim * 4, false) != ACB_OK;
+    if (!err.p) {
+        bad |= err.alloc(4) != ACB_OK;
+    }
+    if (bad) {
+        cap = 0;
+        set_last_error("encoder scratch allocation failed");
+        return ACB_ERR_OOM;
+    }
+    std::vector<int32_t> p((size_t) n);
+    for (int i = 0; i < n; i++) {
+        p[(size_t) i] = i;  // positions 0..S-1 (qwen3-enc.h:418-424)
+    }
+    std::vector<float> tab((size_t) n * c.head_dim);
+    acb_rope_table_host(tab.data(), n, c.head_dim, c.rope_theta);
+    if (cudaMemcpy(pos.p, p.data(), p.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(rope.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    cap = n;
+    return ACB_OK;
+}
+
+// ggml_mul_mat(W, x) for S rows of f32 activations: quantise x like ggml, then the GEMM (with
+// the residual add fused when res is given).
+acb_status acb_qwen3_enc::linear(const Lin & L, const float * x, int64_t xs, int S, void * C, int c_type,
+                                 int64_t ldc, const float * res, cudaStream_t s) {
+    ACB_TRY(acb_act_quant(x, xs, S, L.K, L.vec, xq.p, L.act_type(), L.K, (acb_stream_t) s));
+    return acb_gemm_bf16(xq.p, L.K, L.w, L.K, S, L.N, L.K, C, c_type, ldc, nullptr, res, res ? ldc : 0, nullptr, 0, 0,
+                         kPdl | L.op, err.as<int>(), (acb_stream_t) s);
+}
+
+// The whole forward for S tokens whose ids are already in `ids`; result in `out`.
+acb_status acb_qwen3_enc::enqueue(int S, cudaStream_t s) {
+    const int    H = c.hidden_size, F = c.intermediate_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
+    const int    QD = Nh * D, KD = Nkv * D, NQKV = nqkv();
+    const float  eps   = c.rms_norm_eps;
+    const float  scale = 1.0f / sqrtf((float) D);
+    acb_stream_t as    = (acb_stream_t) s;
+    int *        e     = err.as<int>();
+    float *      hp    = h.as<float>();
+    float *      xp    = xn.as<float>();
+    ACB_TRY(acb_get_rows(embed->data, embed->type, embed->N, H, ids.as<int32_t>(), S, hp, ACB_TYPE_F32, H, e, as));
+    for (const EncLayer & L : layers) {
+        ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.attn_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
+                             as));
+        ACB_TRY(linear(L.qkv, xp, H, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, s));
+        ACB_TRY(acb_qk_norm_rope(qkv.p, ACB_TYPE_F16, NQKV, q.p, ACB_TYPE_F16, QD, D, 0, S, Nh, D,
+                                 (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e, as));
+        ACB_TRY(acb_qk_norm_rope(qkv.as<uint16_t>() + QD, ACB_TYPE_F16, NQKV, k.p, ACB_TYPE_F16, KD, D, 0, S, Nkv, D,
+                                 (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
+                                 as));
+        ACB_TRY(acb_attn_prefill(q.p, (int64_t) S * QD, QD, k.p, (int64_t) S * KD, KD, qkv.as<uint16_t>() + QD + KD,
+                                 (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, 1, S, S, Nh, Nkv,
+                                 D, c.is_causal ? 1 : 0, 0, 0, scale, kPdl | ACB_FLAG_F16, as));
+        ACB_TRY(linear(L.o, att.as<float>(), QD, S, hp, ACB_TYPE_F32, H, hp, s));
+        ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.post_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
+                             as));
+        ACB_TRY(linear(L.gu, xp, H, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, s));
+        ACB_TRY(acb_act_quant_swiglu(gu.as<float>(), 2 * F, F, S, F, L.down.vec, xq.p, L.down.act_type(), F, as));
+        ACB_TRY(acb_gemm_bf16(xq.p, F, L.down.w, F, S, H, F, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
+                              kPdl | L.down.op, e, as));
+    }
+    return acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) final_norm->data, out.p, ACB_TYPE_F32, H, S, H, eps, as);
+}
+
+// Replay (capturing on first use) the graph for S on stream s.
+acb_status acb_qwen3_enc::run(int S, cudaStream_t s) {
+    auto it = graphs.find(S);
+    if (it == graphs.end()) {
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        const acb_status  es = enqueue(S, st);
+        const cudaError_t ce = cudaStreamEndCapture(st, &g);
+        if (es != ACB_OK || ce != cudaSuccess) {
+            if (g) {
+                cudaGraphDestroy(g);
+            }
+            set_last_error("encoder graph capture failed");
+            return es != ACB_OK ? es : ACB_ERR_CUDA;
+        }
+        cudaGraphExec_t   ex = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) {
+            set_last_error("encoder graph instantiation failed");
+            return ACB_ERR_CUDA;
+        }
+        it = graphs.emplace(S, ex).first;
+    }
+    return cudaGraphLaunch(it->second, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
+}
+
+// ---- C ABI ---------------------------------------------------------------------------------------
+
+extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int device, acb_qwen3_enc ** out) {
+    if (!gguf_path || !out) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_last_error("cannot select CUDA device");
+        return ACB_ERR_CUDA;
+    }
+    GGUFFile gf;
+    if (!gf.open(gguf_path)) {
+        set_last_error(gf.error());
+        return gf.error().rfind("cannot open", 0) == 0 ? ACB_ERR_IO : ACB_ERR_FORMAT;
+    }
+    std::unique_ptr<acb_qwen3_enc> m(new acb_qwen3_enc());
+    m->device            = device;
+    acb_qwen3_config & c = m->c;
+    c                    = { 1024, 3072, 16, 8, 128, 28, 1000000.0f, 1e-6f, 1, 0 };  // qwen3-enc.h:327-337
+    const char * j       = gf.get_str("acestep.config_json");
+    if (j && j[0]) {
+        c.hidden_size       = json_int(j, "hidden_size", c.hidden_size);
+        c.intermediate_size = json_int(j, "intermediate_size", c.intermediate_size);
+        c.n_heads           = json_int(j, "num_attention_heads", c.n_heads);
+        c.n_kv_heads        = json_int(j, "num_key_value_heads", c.n_kv_heads);
+        c.head_dim          = json_int(j, "head_dim", c.head_dim);
+        c.n_layers          = json_int(j, "num_hidden_layers", c.n_layers);
+        c.rope_theta        = json_float(j, "rope_theta", c.rope_theta);
+        c.rms_norm_eps      = json_float(j, "rms_norm_eps", c.rms_norm_eps);
+    }
+    auto bad = [&](acb_status s, const std::string & msg) {
+        set_last_error(msg);
+        return s;
+    };
+    const int H = c.hidden_size, F = c.intermediate_size, D = c.head_dim;
+    if (c.n_layers <= 0 || c.n_layers > 64 || D != 128 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads != 0 ||
+        H % 256 != 0 || F % 256 != 0) {
+        return bad(ACB_ERR_UNSUPPORTED, "unsupported encoder configuration");
+    }
+    if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess) {
+        return bad(ACB_ERR_CUDA, "stream creation failed");
+    }
+
+    // Resident tensors: embedding and norms. Linears go through a staging arena that is freed
+    // once their 16-bit copies exist.
+    WeightArena & A     = m->arena;
+    auto          stage = std::make_unique<WeightArena>();
+    m->embed            = A.load(gf, "embed_tokens.weight");
+    m->final_norm       = A.load_f32(gf, "norm.weight");
+    struct Raw {
+        std::vector<DevTensor *> qkv, gu;
+        DevTensor *              o = nullptr, *down = nullptr;
+    };
+    std::vector<Raw> raw((size_t) c.n_layers);
+    m->layers.resize((size_t) c.n_layers);
+    const int QD = c.n_heads * D, KD = c.n_kv_heads * D;
+    for (int i = 0; i < c.n_layers; i++) {
+        const std::string p = "layers." + std::to_string(i);
+        EncLayer &        L = m->layers[(size_t) i];
+        Raw &             R = raw[(size_t) i];
+        L.attn_norm         = A.load_f32(gf, p + ".input_layernorm.weight");
+        L.post_norm         = A.load_f32(gf, p + ".post_attention_layernorm.weight");
+        L.q_norm            = A.load_f32(gf, p + ".self_attn.q_norm.weight");
+        L.k_norm            = A.load_f32(gf, p + ".self_attn.k_norm.weight");
+        R.qkv  = { stage->load(gf, p + ".self_attn.q_proj.weight"), stage->load(gf, p + ".self_attn.k_proj.weight"),
+                   stage->load(gf, p + ".self_attn.v_proj.weight") };
+        R.o    = stage->load(gf, p + ".self_attn.o_proj.weight");
+        R.gu   = { stage->load(gf, p + ".mlp.gate_proj.weight"), stage->load(gf, p + ".mlp.up_proj.weight") };
+        R.down = stage->load(gf, p + ".mlp.down_proj.weight");
+        bool ok = L.attn_norm && L.post_norm && L.q_norm && L.k_norm && R.o && R.down;
+        for (DevTensor * t : R.qkv) {
+            ok = ok && t && t->K == H;
+        }
+        for (DevTensor * t : R.gu) {
+            ok = ok && t && t->K == H && t->N == F;
+        }
+        if (!ok) {
+            return bad(ACB_ERR_FORMAT, !A.error.empty()      ? A.error :
+                                       !stage->error.empty() ? stage->error :
+                                                               "missing or misshapen layer tensor");
+        }
+        if (R.qkv[0]->N != QD || R.qkv[1]->N != KD || R.qkv[2]->N != KD || R.o->K != QD || R.o->N != H ||
+            R.down->K != F || R.down->N != H || L.q_norm->K != D || L.k_norm->K != D || L.attn_norm->K != H) {
+            return bad(ACB_ERR_FORMAT, "layer tensor shapes do not match the config");
+        }
+    }
+    if (!m->embed || !m->final_norm) {
+        return bad(ACB_ERR_FORMAT, A.error);
+    }
+    if (m->embed->K != H) {
+        return bad(ACB_ERR_FORMAT, "embed_tokens shape does not match the config");
+    }
+    c.vocab_size = (int) m->embed->N;
+    ACB_TRY(A.upload(m->st));
+    ACB_TRY(stage->upload(m->st));
+
+    // 16-bit copies, every matrix on a 256-byte boundary
+    const size_t per_layer[4] = { (size_t) (QD + 2 * KD) * H, (size_t) H * QD, (size_t) 2 * F * H, (size_t) H * F };
+    size_t       layer_bytes  = 0;
+    for (size_t n : per_layer) {
+        layer_bytes += (n * 2 + 255) & ~size_t(255);
+    }
+    if (m->w16.alloc(layer_bytes * (size_t) c.n_layers, false) != ACB_OK) {
+        return bad(ACB_ERR_OOM, "16-bit weight allocation failed");
+    }
+    DevBuf        idbuf;
+    const int64_t max_rows = std::max<int64_t>({ (int64_t) QD, (int64_t) F, (int64_t) H });
+    if (idbuf.alloc((size_t) max_rows * 4, false) != ACB_OK) {
+        return bad(ACB_ERR_OOM, "id buffer allocation failed");
+    }
+    {
+        std::vector<int32_t> idv((size_t) max_rows);
+        for (int64_t r = 0; r < max_rows; r++) {
+            idv[(size_t) r] = (int32_t) r;
+        }
+        if (cudaMemcpy(idbuf.p, idv.data(), idv.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            return bad(ACB_ERR_CUDA, "id upload failed");
+        }
+    }
+    // Parts stacked by row concatenation (gf_load_qkv_fused / gf_load_pair_fused,
+    // src/gguf-weights.h:281-354) must share one vec-dot type: the reference only fuses equal
+    // types, and separate matmuls of one activation with different vec-dot types would quantise
+    // it differently.
+    auto build = [&](Lin & L, const std::vector<DevTensor *> & parts, uint16_t * dst) -> acb_status {
+        const int vt = acb_vec_dot_type(parts[0]->type);
+        if (vt < 0) {
+            set_last_error("weight type without a tensor-core path");
+            return ACB_ERR_UNSUPPORTED;
+        }
+        int64_t rows = 0;
+        for (DevTensor * t : parts) {
+            if (acb_vec_dot_type(t->type) != vt) {
+                set_last_error("stacked projections with different vec-dot types");
+                return ACB_ERR_UNSUPPORTED;
+            }
+        }
+        L.w   = dst;
+        L.vec = vt;
+        L.op  = vt == ACB_TYPE_BF16 ? 0 : ACB_FLAG_F16;
+        L.K   = (int) parts[0]->K;
+        for (DevTensor * t : parts) {
+            ACB_TRY(acb_get_rows(t->data, t->type, t->N, t->K, idbuf.as<int32_t>(), t->N, dst + rows * t->K,
+                                 L.act_type(), t->K, nullptr, (acb_stream_t) m->st));
+            rows += t->N;
+        }
+        L.N = (int) rows;
+        return ACB_OK;
+    };
+    uint8_t * base = m->w16.as<uint8_t>();
+    for (int i = 0; i < c.n_layers; i++) {
+        EncLayer & L = m->layers[(size_t) i];
+        Raw &      R = raw[(size_t) i];
+        uint8_t *  p = base + layer_bytes * (size_t) i;
+        uint16_t * w[4];
+        for (int t = 0; t < 4; t++) {
+            w[t] = reinterpret_cast<uint16_t *>(p);
+            p += (per_layer[t] * 2 + 255) & ~size_t(255);
+        }
+        ACB_TRY(build(L.qkv, R.qkv, w[0]));
+        ACB_TRY(build(L.o, { R.o }, w[1]));
+        ACB_TRY(build(L.gu, R.gu, w[2]));
+        ACB_TRY(build(L.down, { R.down }, w[3]));
+    }
+    if (cudaStreamSynchronize(m->st) != cudaSuccess) {
+        return bad(ACB_ERR_CUDA, "weight conversion failed");
+    }
+    stage.reset();
+    ACB_TRY(m->reserve(256));
+    *out = m.release();
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_qwen3_get_config(const acb_qwen3_enc * m, acb_qwen3_config * cfg) {
+    if (!m || !cfg) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    *cfg = m->c;
+    return ACB_OK;
+}
+
+extern "C" size_t acb_qwen3_weight_bytes(const acb_qwen3_enc * m) {
+    return m ? m->arena.bytes() + m->w16.bytes : 0;
+}
+
+extern "C" acb_status acb_qwen3_forward_device(acb_qwen3_enc * m, const int32_t * d_ids, int S, float * d_out,
+                                               acb_stream_t stream) {
+    if (!m || !d_ids || !d_out || S <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->reserve(S));
+    cudaStream_t s = (cudaStream_t) stream;
+    if (cudaMemcpyAsync(m->ids.p, d_ids, (size_t) S * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->run(S, s));
+    const size_t ob = (size_t) S * m->c.hidden_size * 4;
+    return cudaMemcpyAsync(d_out, m->out.p, ob, cudaMemcpyDeviceToDevice, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
+}
+
+static acb_status check_ids(const acb_qwen3_enc * m, const int32_t * ids, int S) {
+    for (int i = 0; i < S; i++) {
+        if (ids[i] < 0 || ids[i] >= m->c.vocab_size) {
+            set_last_error("token id outside the embedding table");
+            return ACB_ERR_OUT_OF_RANGE;
+        }
+    }
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_qwen3_forward(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output) {
+    if (!m || !token_ids || !output || S <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    ACB_TRY(check_ids(m, token_ids, S));
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->reserve(S));
+    if (cudaMemcpyAsync(m->ids.p, token_ids, (size_t) S * 4, cudaMemcpyHostToDevice, m->st) != cudaSuccess ||
+        cudaMemsetAsync(m->err.p, 0, 4, m->st) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->run(S, m->st));
+    int          dev_err = 0;
+    const size_t ob      = (size_t) S * m->c.hidden_size * 4;
+    if (cudaMemcpyAsync(output, m->out.p, ob, cudaMemcpyDeviceToHost, m->st) != cudaSuccess ||
+        cudaMemcpyAsync(&dev_err, m->err.p, 4, cudaMemcpyDeviceToHost, m->st) != cudaSuccess ||
+        cudaStreamSynchronize(m->st) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    if (dev_err) {
+        set_last_error("device error flag " + std::to_string(dev_err));
+        return ACB_ERR_DEVICE;
+    }
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_qwen3_embed_lookup(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output) {
+    if (!m || !token_ids || !output || S <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    ACB_TRY(check_ids(m, token_ids, S));
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->reserve(S));
+    const int H = m->c.hidden_size;
+    if (cudaMemcpyAsync(m->ids.p, token_ids, (size_t) S * 4, cudaMemcpyHostToDevice, m->st) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(acb_get_rows(m->embed->data, m->embed->type, m->embed->N, H, m->ids.as<int32_t>(), S, m->out.p,
+                         ACB_TYPE_F32, H, nullptr, (acb_stream_t) m->st));
+    if (cudaMemcpyAsync(output, m->out.p, (size_t) S * H * 4, cudaMemcpyDeviceToHost, m->st) != cudaSuccess ||
+        cudaStreamSynchronize(m->st) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+extern "C" void acb_qwen3_free(acb_qwen3_enc * m) {
+    delete m;
+}

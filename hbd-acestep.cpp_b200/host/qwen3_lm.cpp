@@ -23,11 +23,8 @@
 
 #include "../../include/acb_models.h"
 #include "gguf.h"
+#include "host_common.h"
 #include "weights.h"
-
-namespace acb {
-void set_last_error(const std::string & e);
-}
 
 using namespace acb;
 
@@ -38,41 +35,6 @@ struct LMLayer {
     DevTensor *qkv = nullptr, *qk = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *o = nullptr;
     DevTensor *gate_up = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
 };
-
-// Value text of "key": in a flat JSON object (the lookup of qw3lm_json_int/_float/_bool,
-// src/qwen3-lm.h:60-121), or nullptr.
-const char * json_value(const char * j, const char * key) {
-    char needle[128];
-    snprintf(needle, sizeof(needle), "\"%s\"", key);
-    const char * p = strstr(j, needle);
-    if (!p) {
-        return nullptr;
-    }
-    p = strchr(p + strlen(needle), ':');
-    if (!p) {
-        return nullptr;
-    }
-    p++;
-    while (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r') {
-        p++;
-    }
-    return p;
-}
-
-int json_int(const char * j, const char * key, int fb) {
-    const char * v = json_value(j, key);
-    return v ? atoi(v) : fb;
-}
-
-float json_float(const char * j, const char * key, float fb) {
-    const char * v = json_value(j, key);
-    return v ? (float) atof(v) : fb;
-}
-
-bool json_bool(const char * j, const char * key, bool fb) {
-    const char * v = json_value(j, key);
-    return v ? strncmp(v, "true", 4) == 0 : fb;
-}
 
 constexpr int kPrefillChunk = 256;  // tokens per prefill pass
 constexpr int kMaxSets      = 32;   // QW3LM_MAX_KV_SETS (qwen3-lm.h:29)
@@ -141,14 +103,6 @@ acb_status gemv_rows(acb_qw3lm * m, const DevTensor * W, int64_t row0, int64_t n
     }
     return ACB_OK;
 }
-
-#define ACB_TRY(x)                 \
-    do {                           \
-        const acb_status s_ = (x); \
-        if (s_ != ACB_OK) {        \
-            return s_;             \
-        }                          \
-    } while (0)
 
 // Layers for n tokens whose embeddings are in m->hidden and positions in m->pos.
 acb_status enqueue_layers(acb_qw3lm * m, int n, int set0, int set_per_tok) {

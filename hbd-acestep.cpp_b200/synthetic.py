@@ -21,6 +21,9 @@ Q8_0, Q4_K, Q6_K, F32 = acb.Q8_0, acb.Q4_K, acb.Q6_K, acb.F32
 QWEN3_1_7B = dict(vocab_size=217472, hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
                   num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1000000.0,
                   rms_norm_eps=1e-6, tie_word_embeddings=True)
+QWEN3_EMBED_0_6B = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                        num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1000000.0,
+                        rms_norm_eps=1e-6)
 QWEN3_4B = dict(vocab_size=217472, hidden_size=2560, intermediate_size=9728, num_hidden_layers=36,
                 num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1000000.0,
                 rms_norm_eps=1e-6, tie_word_embeddings=True)
@@ -51,8 +54,9 @@ def quantize_on_device(w, qtype: int):
     return out.cpu().numpy()
 
 
-def lm_tensors(cfg: dict, policy=policy_q8_0, seed: int = 0, device: str = "cuda"):
-    """Yields (name, qtype, raw uint8 [N, row_bytes] or float32 array, ggml K) in file order."""
+def lm_tensors(cfg: dict, policy=policy_q8_0, seed: int = 0, device: str = "cuda", prefix: str = "model."):
+    """Yields (name, qtype, raw uint8 [N, row_bytes] or float32 array, ggml K) in file order.
+    prefix "model." gives the LM's names (src/qwen3-lm.h), "" the text encoder's (src/qwen3-enc.h)."""
     import torch
     g = torch.Generator(device=device).manual_seed(seed)
     H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
@@ -67,10 +71,10 @@ def lm_tensors(cfg: dict, policy=policy_q8_0, seed: int = 0, device: str = "cuda
         v = (1.0 + 0.01 * torch.randn(n, generator=g, device=device)).cpu().numpy().astype(np.float32)
         return name, F32, v, n
 
-    yield mat("model.embed_tokens.weight", V, H, -1)
-    yield gain("model.norm.weight", H)
+    yield mat(f"{prefix}embed_tokens.weight", V, H, -1)
+    yield gain(f"{prefix}norm.weight", H)
     for i in range(L):
-        p = f"model.layers.{i}"
+        p = f"{prefix}layers.{i}"
         yield gain(f"{p}.input_layernorm.weight", H)
         yield gain(f"{p}.post_attention_layernorm.weight", H)
         yield mat(f"{p}.self_attn.q_proj.weight", Nh * D, H, i)
@@ -85,14 +89,15 @@ def lm_tensors(cfg: dict, policy=policy_q8_0, seed: int = 0, device: str = "cuda
 
 
 def write_lm_gguf(path: str, cfg: dict, policy=policy_q8_0, seed: int = 0, device: str = "cuda",
-                  keep: dict | None = None) -> int:
-    """Write a Qwen3 LM GGUF (arch acestep-lm). If `keep` is a dict, the raw tensors are stored in
-    it by name (for oracle comparisons on small models). Returns the file's tensor-data bytes."""
+                  keep: dict | None = None, prefix: str = "model.", arch: str = "acestep-lm") -> int:
+    """Write a Qwen3 LM GGUF (arch acestep-lm; prefix "" and arch "qwen3" for a text encoder).
+    If `keep` is a dict, the raw tensors are stored in it by name (for oracle comparisons on
+    small models). Returns the file's tensor-data bytes."""
     import gguf
-    w = gguf.GGUFWriter(path, "acestep-lm")
+    w = gguf.GGUFWriter(path, arch)
     w.add_string("acestep.config_json", json.dumps(cfg))
     total = 0
-    for name, qt, raw, K in lm_tensors(cfg, policy, seed, device):
+    for name, qt, raw, K in lm_tensors(cfg, policy, seed, device, prefix):
         if qt == F32:
             w.add_tensor(name, raw)
         else:

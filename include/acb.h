@@ -138,13 +138,44 @@ ACB_API acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int ty
 
 /* ---- dense path (configs 1, 4, 5): tensor-core GEMM ---------------------------------------- */
 
+enum {
+    ACB_FLAG_F16 = 2, /* acb_gemm_bf16 / acb_attn_prefill: the tensor-core operands are f16, not bf16 */
+};
+
+/* Activation operand of a tensor-core linear, with the arithmetic of ggml-CPU's quantised
+ * mul_mat: each f32 row of x [rows][x_stride] is quantised like ggml's from_float for the
+ * weight's vec-dot type and the dequantised values d*q are written rounded to f16, so that a
+ * GEMM of f16 operands reproduces the reference's products up to f16 rounding:
+ *   vec_type ACB_TYPE_Q8_0 (weights Q8_0): per 32, d = amax/127 stored as f16, q = round(x/d);
+ *   vec_type ACB_TYPE_Q8_K (weights Q4_K / Q6_K): per 256, the signed value of largest magnitude
+ *            mx (first index), iscale = -127/mx, q = min(127, round-half-even(iscale*x)),
+ *            d = 1/iscale;
+ *   vec_type ACB_TYPE_F16 / ACB_TYPE_BF16 (weights of that type): x rounded to that type.
+ * y_type is ACB_TYPE_BF16 for vec_type BF16, else ACB_TYPE_F16. K a multiple of 32 (256 for
+ * Q8_K). Replaces the activation quantisation inside ggml_mul_mat (src/qwen3-enc.h:86-88,
+ * src/dit-graph.h:36-49) at M = tokens. */
+ACB_API acb_status acb_act_quant(const float * x, int64_t x_stride, int64_t rows, int64_t K, int vec_type, void * y,
+                                 int y_type, int64_t y_stride, acb_stream_t stream);
+
+/* acb_act_quant of h = silu(g) * u (the ggml_swiglu arithmetic of acb_swiglu) over fused rows:
+ * g = gu + r*gu_stride, u = g + up_offset, F columns; the activation of the down projection. */
+ACB_API acb_status acb_act_quant_swiglu(const float * gu, int64_t gu_stride, int64_t up_offset, int64_t rows,
+                                        int64_t F, int vec_type, void * y, int y_type, int64_t y_stride,
+                                        acb_stream_t stream);
+
+/* Vec-dot type of a weight type (ggml's type_traits_cpu[].vec_dot_type): Q8_0 for Q8_0, Q8_K
+ * for Q4_K / Q6_K, the type itself for F16 / BF16; -1 for types without a tensor-core path. */
+ACB_API int acb_vec_dot_type(int weight_type);
+
 /* C[m][n] = epi(sum_k A[m][k] B[n][k]) on the 5th-generation tensor cores (tcgen05.mma, TMEM
- * accumulators, TMA-fed 128-byte-swizzled tiles): A [M][lda] and B [N][ldb] bf16 row-major
- * (K contiguous, K a multiple of 64, rows 16-byte aligned), fp32 accumulation, C f32 or bf16
- * [M][ldc]. Epilogue, applied in order: + bias[n] (f32, optional); then with res (f32 [M][ldr],
- * may alias an f32 C): C = res + acc, or with gate (f32, row m uses gate[(m / rows_per_sample) *
- * gate_stride + n]): C = res + acc * gate, the DiT gated residual. B holds the weights
- * dequantised once to bf16 (acb_get_rows with identity ids). Replaces ggml_mul_mat at M = tokens
+ * accumulators, TMA-fed 128-byte-swizzled tiles): A [M][lda] and B [N][ldb] bf16 row-major, or
+ * f16 with ACB_FLAG_F16 (K contiguous, K a multiple of 64, rows 16-byte aligned), fp32
+ * accumulation, C f32, bf16 or f16 [M][ldc]. Epilogue, applied in order: + bias[n] (f32,
+ * optional); then with res (f32 [M][ldr], may alias an f32 C): C = res + acc, or with gate (f32,
+ * row m uses gate[(m / rows_per_sample) * gate_stride + n]): C = res + acc * gate, the DiT gated
+ * residual. B holds the weights dequantised once (acb_get_rows with identity ids; f16 for
+ * quantised and F16 weights, bf16 for BF16 weights) and A comes from acb_act_quant, which
+ * together give ggml's quantised mul_mat up to f16 rounding. Replaces ggml_mul_mat at M = tokens
  * in dit_ggml_linear(_bias) (src/dit-graph.h:36-49), the DiT layer's projections
  * (dit-graph.h:159-172, 258-268, 298-314) with dit_ggml_gated_add (:70-76) fused, and the
  * encoder's prefill linears (src/qwen3-enc.h:86-88). */
@@ -153,13 +184,14 @@ ACB_API acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, in
                                  int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
                                  int flags, int * err_flag, acb_stream_t stream);
 
-/* Attention over whole sequences (flash tiling on bf16 tensor cores, fp32 softmax and
+/* Attention over whole sequences (flash tiling on tensor cores, fp32 softmax and
  * accumulation), head_dim 128, GQA head h -> kv head h / (Nh/Nkv):
  *   O[b,i,h] = softmax_j(Q[b,i,h].K[b,j,h'] * scale + mask) V[b,j,h']
- * Q/K/V bf16 with element strides per batch (*_bs) and per token (*_ts); heads are contiguous
+ * Q/K/V bf16 (f16 with ACB_FLAG_F16; the probabilities then meet V in the same type) with
+ * element strides per batch (*_bs) and per token (*_ts); heads are contiguous
  * 128-element runs within a token row (so Q, K and V may be column views of one fused QKV
  * row). mask: 0 none, 1 causal (key j <= i + causal_off), 2 sliding window (|i - j| <= window).
- * O is f32 or bf16. Replaces ggml_flash_attn_ext / qwen3_attn_f32 / dit_attn_f32 at prefill
+ * O is f32, bf16 or f16. Replaces ggml_flash_attn_ext / qwen3_attn_f32 / dit_attn_f32 at prefill
  * (src/qwen3-enc.h:186-199; src/dit-graph.h:218-231 self-attention with the sliding-window and
  * padding masks of dit-sampler.h:253-282, and 339-352 cross-attention). */
 ACB_API acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs,

@@ -31,6 +31,52 @@ ACB_API const char * acb_gguf_get_str(const acb_gguf * g, const char * key);    
 ACB_API int          acb_gguf_get_bool(const acb_gguf * g, const char * key);    /* gf_get_bool :387 */
 ACB_API const char * acb_last_error(void); /* message of the last failed load in this thread */
 
+/* ---- Qwen3 encoder stack (replaces src/qwen3-enc.h) ------------------------------------------ */
+
+typedef struct acb_qwen3_enc acb_qwen3_enc;
+
+/* Qwen3Config (qwen3-enc.h:27-37) plus the embedding table's row count. */
+typedef struct {
+    int   hidden_size;
+    int   intermediate_size;
+    int   n_heads;
+    int   n_kv_heads;
+    int   head_dim;
+    int   n_layers;
+    float rope_theta;
+    float rms_norm_eps;
+    int   is_causal;
+    int   vocab_size;
+} acb_qwen3_config;
+
+/* qwen3_load_text_encoder (qwen3-enc.h:319-367): tensors embed_tokens.weight, norm.weight and
+ * layers.N.* (no "model." prefix), config 1024/3072/16/8/128/28 layers, rope theta 1e6,
+ * eps 1e-6, causal -- the reference's constants; a GGUF carrying acestep.config_json may
+ * override them (the shipped text encoder's config holds the same values). Every linear is
+ * dequantised once to a resident f16 copy (bf16 for BF16 weights; Q||K||V and gate||up stacked
+ * into one matrix) for the tensor-core GEMM, whose activations are quantised like ggml's
+ * quantised mul_mat (acb_act_quant); the embedding table and norms keep their GGUF / F32
+ * forms. `device` is the CUDA ordinal the model lives on. */
+ACB_API acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int device, acb_qwen3_enc ** out);
+ACB_API acb_status acb_qwen3_get_config(const acb_qwen3_enc * m, acb_qwen3_config * cfg);
+ACB_API size_t     acb_qwen3_weight_bytes(const acb_qwen3_enc * m); /* device bytes of all weights */
+
+/* qwen3_forward (qwen3-enc.h:373-448): token ids (host, [S]) -> last-layer hidden states after
+ * the final RMSNorm (host, caller-allocated [S][hidden_size] f32). ACB_ERR_OUT_OF_RANGE when an
+ * id is outside the embedding table. */
+ACB_API acb_status acb_qwen3_forward(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output);
+
+/* The same forward on device buffers (ids [S] int32, out [S][hidden_size] f32), enqueued on
+ * `stream` without a host synchronisation. The chain for each S is captured once as a CUDA
+ * graph over the model's own scratch, so calls on one model must not overlap. Ids are not
+ * range-checked on the host here; acb_qwen3_forward is the checked entry point. */
+ACB_API acb_status acb_qwen3_forward_device(acb_qwen3_enc * m, const int32_t * d_ids, int S, float * d_out,
+                                            acb_stream_t stream);
+
+/* qwen3_embed_lookup (qwen3-enc.h:453-480): embedding rows (host ids [S] -> host [S][H] f32). */
+ACB_API acb_status acb_qwen3_embed_lookup(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output);
+ACB_API void       acb_qwen3_free(acb_qwen3_enc * m); /* qwen3_free :483 */
+
 /* ---- Qwen3 causal LM (replaces src/qwen3-lm.h) ---------------------------------------------- */
 
 typedef struct acb_qw3lm acb_qw3lm;

@@ -686,12 +686,57 @@ static float dot_q6_K_q8_K(const uint8_t * w, const uint8_t * xq, int64_t nb) {
     return sumf;
 }
 
+static int g_mm_mode = ORC_MM_GGML;
+
+void orc_set_mul_mat_mode(int mode) {
+    g_mm_mode = mode == ORC_MM_EXACT ? ORC_MM_EXACT : ORC_MM_GGML;
+}
+
+int orc_get_mul_mat_mode(void) {
+    return g_mm_mode;
+}
+
+/* ORC_MM_EXACT: every weight row dequantised once, f32 activation, double accumulation. */
+static int mul_mat_exact(int wtype, const uint8_t * w, int64_t rb, int64_t N, int64_t K, const float * x, int64_t M,
+                         float * y) {
+    float * wd = (float *) malloc(sizeof(float) * (size_t) (N * K));
+    if (!wd) {
+        return -1;
+    }
+    int bad = 0;
+#pragma omp parallel for schedule(static) reduction(| : bad)
+    for (int64_t n = 0; n < N; n++) {
+        bad |= orc_dequant_row(wtype, w + n * rb, wd + n * K, K) != 0;
+    }
+    if (bad) {
+        free(wd);
+        return -1;
+    }
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int64_t m = 0; m < M; m++) {
+        for (int64_t n = 0; n < N; n++) {
+            const float * xr  = x + m * K;
+            const float * wr  = wd + n * K;
+            double        acc = 0.0;
+            for (int64_t k = 0; k < K; k++) {
+                acc += (double) wr[k] * (double) xr[k];
+            }
+            y[m * N + n] = (float) acc;
+        }
+    }
+    free(wd);
+    return 0;
+}
+
 int orc_mul_mat(int wtype, const void * W, int64_t N, int64_t K, const float * x, int64_t M, float * y) {
     int64_t rb = orc_row_bytes(wtype, K);
     if (rb < 0) {
         return -1;
     }
     const uint8_t * w = (const uint8_t *) W;
+    if (g_mm_mode == ORC_MM_EXACT) {
+        return mul_mat_exact(wtype, w, rb, N, K, x, M, y);
+    }
     if (wtype == ORC_Q8_0 || wtype == ORC_Q4_K || wtype == ORC_Q6_K) {
         int     vt  = wtype == ORC_Q8_0 ? ORC_Q8_0 : ORC_Q8_K;
         int64_t xrb = orc_row_bytes(vt, K);

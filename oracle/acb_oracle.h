@@ -101,6 +101,16 @@ void orc_gated_residual(const float * r, const float * o, const float * gate, in
  * W: N rows of K elements in wtype (Q8_0, Q4_K, Q6_K, BF16, F16, F32). */
 int orc_mul_mat(int wtype, const void * W, int64_t N, int64_t K, const float * x, int64_t M, float * y);
 
+/* Arithmetic of orc_mul_mat, process-wide:
+ *   ORC_MM_GGML  (default) ggml-CPU semantics: the activation is quantised to the weight's
+ *                vec-dot type (Q8_0 / Q8_K) or rounded to F16 / BF16 before the dot products;
+ *   ORC_MM_EXACT dequantised weights times the unrounded f32 activation, accumulated in double.
+ * EXACT measures how far the reference's own activation quantisation sits from exact
+ * arithmetic; GGML is the reference every parity bar is taken against. */
+enum { ORC_MM_GGML = 0, ORC_MM_EXACT = 1 };
+void orc_set_mul_mat_mode(int mode);
+int  orc_get_mul_mat_mode(void);
+
 /* Attention with ggml-CPU semantics of qwen3_attn_f32 (qwen3-enc.h:101-112).
  * q [Sq][Hq][D] f32; k/v in kv_type (F32 or F16): element (token j, head h, d) at
  * j*kv_tok_stride + h*kv_head_stride + d;

@@ -56,6 +56,8 @@ def lib():
             "orc_attention": (None, [P, I64, P, P, I, I64, I64, P, P, I64, I64, I64, I, I, I, F]),
             "orc_timestep_embedding": (None, [F, I, I, P]),
             "orc_set_threads": (None, [I]),
+            "orc_set_mul_mat_mode": (None, [I]),
+            "orc_get_mul_mat_mode": (I, []),
             "orc_get_threads": (I, []),
         }
         for name, (res, args) in sig.items():
@@ -86,6 +88,33 @@ def set_threads(n: int) -> None:
 
 def get_threads() -> int:
     return lib().orc_get_threads()
+
+
+MM_GGML, MM_EXACT = 0, 1
+
+
+def set_mul_mat_mode(mode: int) -> None:
+    """MM_GGML: ggml-CPU quantized mul_mat (activation quantised to Q8_0 / Q8_K); MM_EXACT:
+    dequantised weights times the f32 activation in double."""
+    lib().orc_set_mul_mat_mode(int(mode))
+
+
+def get_mul_mat_mode() -> int:
+    return lib().orc_get_mul_mat_mode()
+
+
+class mul_mat_mode:
+    """Context manager: `with mul_mat_mode(MM_EXACT): ...` restores the previous mode."""
+
+    def __init__(self, mode):
+        self.mode = mode
+
+    def __enter__(self):
+        self.prev = get_mul_mat_mode()
+        set_mul_mat_mode(self.mode)
+
+    def __exit__(self, *a):
+        set_mul_mat_mode(self.prev)
 
 
 # ---- formats -------------------------------------------------------------------------------
@@ -402,14 +431,15 @@ class OracleDiT:
         return out
 
 
-def qwen3_from_gguf_tensors(cfg, tensors):
+def qwen3_from_gguf_tensors(cfg, tensors, prefix="model."):
     """OracleQwen3 over raw GGUF tensors {name: (qtype, raw, K, N)} with the reference names
-    (model.layers.{i}.self_attn.q_proj.weight, ...), fused like gf_load_qkv_fused /
-    gf_load_pair_fused (src/gguf-weights.h:281-354) when the types match."""
+    (model.layers.{i}.self_attn.q_proj.weight, ...; prefix "" for the text encoder's
+    layers.{i}...), fused like gf_load_qkv_fused / gf_load_pair_fused
+    (src/gguf-weights.h:281-354) when the types match."""
     L = cfg["num_hidden_layers"]
-    w = {"embed": tensors["model.embed_tokens.weight"], "final_norm": tensors["model.norm.weight"]}
+    w = {"embed": tensors[f"{prefix}embed_tokens.weight"], "final_norm": tensors[f"{prefix}norm.weight"]}
     for i in range(L):
-        p = f"model.layers.{i}"
+        p = f"{prefix}layers.{i}"
         w[f"layers.{i}.attn_norm"] = tensors[f"{p}.input_layernorm.weight"]
         w[f"layers.{i}.post_norm"] = tensors[f"{p}.post_attention_layernorm.weight"]
         w[f"layers.{i}.q_norm"] = tensors[f"{p}.self_attn.q_norm.weight"]

@@ -25,7 +25,8 @@ def policy_q4_k_m(name, layer, L):
     return O.Q4_K
 
 
-def make_tensors(cfg, policy, seed=0, std=0.02, embed_std=None):
+def make_tensors(cfg, policy, seed=0, std=0.02, embed_std=None, prefix="model."):
+    """prefix "model." gives the LM's tensor names, "" the text encoder's."""
     rng = np.random.default_rng(seed)
     H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"]
     Nh, Nkv, D, V = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"], cfg["vocab_size"]
@@ -39,10 +40,10 @@ def make_tensors(cfg, policy, seed=0, std=0.02, embed_std=None):
     def gain(name, n):
         out[name] = (O.F32, (1.0 + 0.01 * rng.standard_normal(n)).astype(np.float32), n, 1)
 
-    mat("model.embed_tokens.weight", V, H, -1, embed_std or std)
-    gain("model.norm.weight", H)
+    mat(f"{prefix}embed_tokens.weight", V, H, -1, embed_std or std)
+    gain(f"{prefix}norm.weight", H)
     for i in range(L):
-        p = f"model.layers.{i}"
+        p = f"{prefix}layers.{i}"
         gain(f"{p}.input_layernorm.weight", H)
         gain(f"{p}.post_attention_layernorm.weight", H)
         mat(f"{p}.self_attn.q_proj.weight", Nh * D, H, i)
@@ -57,9 +58,9 @@ def make_tensors(cfg, policy, seed=0, std=0.02, embed_std=None):
     return out
 
 
-def write_gguf(path, cfg, tensors):
+def write_gguf(path, cfg, tensors, arch="acestep-lm"):
     import gguf
-    w = gguf.GGUFWriter(path, "acestep-lm")
+    w = gguf.GGUFWriter(path, arch)
     w.add_string("acestep.config_json", json.dumps(cfg))
     for name, (qt, raw, K, N) in tensors.items():
         if qt == O.F32:
@@ -72,8 +73,8 @@ def write_gguf(path, cfg, tensors):
     w.close()
 
 
-def oracle_model(cfg, tensors):
-    return O.qwen3_from_gguf_tensors(cfg, tensors)
+def oracle_model(cfg, tensors, prefix="model."):
+    return O.qwen3_from_gguf_tensors(cfg, tensors, prefix)
 
 
 def oracle_greedy(m, prompt, n_steps, set_=0):

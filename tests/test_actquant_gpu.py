@@ -1,0 +1,60 @@
+"""GPU: the activation operand of the tensor-core linears (acb_act_quant, acb_act_quant_swiglu)
+against the oracle's ggml activation quantisers. The kernel writes fp16(d*q) for each element
+of each Q8_0 / Q8_K block: the oracle's quantise -> dequantise values rounded to f16 must match
+bit for bit (integer and scale arithmetic identical, one rounding at the end)."""
+import numpy as np
+import pytest
+
+import acb
+import oracle as O
+from helpers import assert_bitexact
+
+pytestmark = pytest.mark.gpu
+
+
+def ref_fq(x, vt):
+    """Oracle: ggml from_float for vec_type vt, dequantised to f32, then rounded to the operand type."""
+    if vt == O.Q8_0:
+        return O.dequantize(O.quantize(x, O.Q8_0), O.Q8_0, x.shape[1]).astype(np.float16)
+    if vt == O.Q8_K:
+        raw = O.quantize(x, O.Q8_K).reshape(x.shape[0], -1, 292)
+        d = raw[:, :, 0:4].copy().view(np.float32)             # [rows, blocks, 1]
+        q = raw[:, :, 4:260].view(np.int8).astype(np.float32)  # [rows, blocks, 256]
+        return (d * q).astype(np.float32).reshape(x.shape).astype(np.float16)
+    if vt == O.F16:
+        return x.astype(np.float16)
+    return O.bf16_bits_to_f32(O.f32_to_bf16_bits(x))
+
+
+@pytest.mark.parametrize("vt", [O.Q8_0, O.Q8_K, O.F16, O.BF16])
+@pytest.mark.parametrize("M,K", [(1, 256), (77, 1024), (256, 3072), (33, 6144)])
+def test_act_quant_matches_oracle(cuda, vt, M, K):
+    import torch
+    rng = np.random.default_rng(M * K + vt)
+    x = (rng.standard_normal((M, K)) * rng.uniform(0.1, 30, (M, 1))).astype(np.float32)
+    x[0, :64] = 0.0  # an all-zero Q8_0 block (d = 0)
+    if K == 256:
+        x[-1, :] = 0.0  # an all-zero Q8_K block
+    y = acb.act_quant(torch.from_numpy(x).to(cuda), vt)
+    want = ref_fq(x, vt)
+    got = y.cpu()
+    got = got.float().numpy() if vt == O.BF16 else got.numpy()
+    assert_bitexact(got, want, f"act_quant vt={vt}")
+
+
+@pytest.mark.parametrize("vt", [O.Q8_0, O.Q8_K])
+def test_act_quant_swiglu_matches_oracle(cuda, vt):
+    import torch
+    rng = np.random.default_rng(vt)
+    M, F = 65, 3072
+    gu = (rng.standard_normal((M, 2 * F)) * 2).astype(np.float32)
+    y = acb.act_quant_swiglu(torch.from_numpy(gu).to(cuda), F, vt)
+    h = O.swiglu(gu[:, :F], gu[:, F:])
+    assert_bitexact(y.cpu().numpy(), ref_fq(h, vt), "act_quant_swiglu")
+
+
+def test_vec_dot_types():
+    assert acb.vec_dot_type(acb.Q8_0) == acb.Q8_0
+    assert acb.vec_dot_type(acb.Q4_K) == acb.Q8_K and acb.vec_dot_type(acb.Q6_K) == acb.Q8_K
+    assert acb.vec_dot_type(acb.F16) == acb.F16 and acb.vec_dot_type(acb.BF16) == acb.BF16
+    assert acb.vec_dot_type(acb.F32) == -1

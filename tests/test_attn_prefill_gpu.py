@@ -73,3 +73,27 @@ def test_attn_prefill_views_of_fused_qkv_and_oracle(cuda):
     ref = O.attention(qn, kn, vn, O.F32, mask, 1.0 / math.sqrt(128)).reshape(S, Nh * 128)
     got = o[0].cpu().numpy()
     assert cos_sim(got, ref) >= 0.9999 and max_rel(got, ref) <= 1e-2
+
+
+@pytest.mark.parametrize("B,Sq,Skv,Nh,Nkv,mask,window", [
+    (1, 256, 256, 16, 8, acb.MASK_CAUSAL, 0),
+    (8, 750, 750, 16, 8, acb.MASK_WINDOW, 128),
+    (8, 750, 512, 16, 8, acb.MASK_NONE, 0),
+    (2, 77, 33, 4, 2, acb.MASK_NONE, 0),
+])
+def test_attn_prefill_f16_operands(cuda, B, Sq, Skv, Nh, Nkv, mask, window):
+    """ACB_FLAG_F16: f16 Q/K/V and f16 probabilities (11-bit significands): bar cosine >= 0.99999
+    and max_rel <= 2e-3 against the fp32 softmax attention of the same operands."""
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(Sq * 3 + Skv + mask)
+    q = (torch.randn(B, Sq, Nh * 128, device=cuda, generator=g) * 1.5).half()
+    k = (torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g) * 1.5).half()
+    v = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g).half()
+    o = acb.attn_prefill(q, k, v, Nh, Nkv, mask=mask, window=window, out_dtype=torch.float32)
+    ref = torch_ref(q, k, v, Nh, Nkv, mask, window, 0)
+    got, want = o.cpu().numpy(), ref.cpu().numpy()
+    for b in range(B):
+        c, r = cos_sim(got[b], want[b]), max_rel(got[b], want[b])
+        assert c >= 0.99999 and r <= 2e-3, (b, c, r)
+    oh = acb.attn_prefill(q, k, v, Nh, Nkv, mask=mask, window=window, out_dtype=torch.float16)
+    assert max_rel(oh.float().cpu().numpy(), got) <= 2.0 ** -10

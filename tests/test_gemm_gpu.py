@@ -61,3 +61,22 @@ def test_gemm_epilogues(cuda):
     Cb = acb.gemm_bf16(A, B, out_dtype=torch.bfloat16)
     d = (Cb.float() - base).abs()
     assert (d <= base.abs() * 2.0 ** -8 + 1e-6).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 4096, 1024), (77, 300, 128), (6000, 2048, 6144)])
+def test_gemm_f16_operands(cuda, M, N, K):
+    """ACB_FLAG_F16: the same GEMM on f16 operands (the reference-faithful dense path), f32 and
+    f16 output."""
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    A = torch.randn(M, K, device=cuda, generator=g).half()
+    B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).half()
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    C = acb.gemm_bf16(A, B, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = ref_mm(A, B)
+    assert max_rel(C.cpu().numpy(), ref.cpu().numpy()) <= 1e-5
+    Ch = acb.gemm_bf16(A, B, out_dtype=torch.float16)
+    d = (Ch.float() - ref).abs()
+    assert (d <= ref.abs() * 2.0 ** -10 + 2e-5 * ref.abs().max()).all()

@@ -144,3 +144,21 @@ def test_oracle_decode_matches_prefill():
     b.alloc_kv(1, 64)
     full = b.prefill(prompt)
     assert cos_sim(dec[0], full) > 0.999999
+
+
+def test_mul_mat_exact_mode_is_dequantised_float_product():
+    """ORC_MM_EXACT: dequantised weights times the unrounded activation (double accumulation);
+    ORC_MM_GGML stays the default and differs by the activation quantisation."""
+    rng = np.random.default_rng(11)
+    N, K, M = 40, 512, 3
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    assert O.get_mul_mat_mode() == O.MM_GGML
+    for qt in (O.Q8_0, O.Q4_K, O.Q6_K, O.BF16):
+        W = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), qt)
+        ref = x.astype(np.float64) @ O.dequantize(W, qt, K).astype(np.float64).T
+        with O.mul_mat_mode(O.MM_EXACT):
+            y = O.mul_mat(qt, W, N, K, x)
+        assert np.abs(y - ref).max() <= 1e-6 * np.abs(ref).max()
+        g = O.mul_mat(qt, W, N, K, x)
+        assert np.abs(g - ref).max() > 0  # the ggml mode rounds the activation
+    assert O.get_mul_mat_mode() == O.MM_GGML
