@@ -642,11 +642,13 @@ def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
     torch.cuda.synchronize()
     # the 0.9 GB of f16 weights exceed the 126 MB L2: back-to-back forwards stream them from HBM
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()  # profiler range = the timed forwards (no effect without a profiler)
     e0.record(stream)
     for _ in range(reps):
         enc.forward_device(d_ids, d_out, stream)
     e1.record(stream)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1) / reps
     fl = enc_flops(cfg, S)
     # e2e: host ids in, host hidden states out (acb_qwen3_forward, the qwen3_forward drop-in)

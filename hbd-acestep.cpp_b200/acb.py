@@ -98,6 +98,7 @@ def lib():
             "acb_qwen3_forward": (I, [P, P, I, P]),
             "acb_qwen3_forward_device": (I, [P, P, I, P, P]),
             "acb_qwen3_embed_lookup": (I, [P, P, I, P]),
+            "acb_qwen3_forward_hidden": (I, [P, P, I, I, I, I, P, P]),
             "acb_qwen3_free": (None, [P]),
             "acb_act_quant": (I, [P, I64, I64, I64, I, P, I, I64, P]),
             "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
@@ -474,6 +475,16 @@ class Qwen3Encoder:
         """Device int32 ids [S] -> device f32 out [S][H], enqueued on the stream."""
         _check("acb_qwen3_forward_device", lib().acb_qwen3_forward_device(
             self.h, _ptr(ids), ids.numel(), _ptr(out), _stream(stream)))
+        return out
+
+    def forward_hidden(self, hidden, layer_begin, layer_end, final_norm=False, out=None, stream=None):
+        """Layers [layer_begin, layer_end) from device f32 hidden [S][H] -> device f32 [S][H]."""
+        import torch
+        if out is None:
+            out = torch.empty_like(hidden)
+        _check("acb_qwen3_forward_hidden", lib().acb_qwen3_forward_hidden(
+            self.h, _ptr(hidden), hidden.shape[0], layer_begin, layer_end, int(final_norm), _ptr(out),
+            _stream(stream)))
         return out
 
     def embed_lookup(self, ids):

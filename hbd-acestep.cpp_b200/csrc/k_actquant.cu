@@ -75,7 +75,8 @@ __global__ void __launch_bounds__(kAqWarps * 32)
         const float dh = __half2float(__float2half_rn(d));  // the block stores d as f16
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            o[e] = __fmul_rn(dh, roundf(__fmul_rn(v[e], id)));
+            // through an int, as the block stores it: a rounded -0.x is +0
+            o[e] = __fmul_rn(dh, (float) (int) roundf(__fmul_rn(v[e], id)));
         }
     } else if (VT == ACB_TYPE_Q8_K) {
         float amax = 0.0f, mx = 0.0f;

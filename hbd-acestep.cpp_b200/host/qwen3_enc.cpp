@@ -91,6 +91,7 @@ struct acb_qwen3_enc {
     acb_status reserve(int S);
     acb_status linear(const Lin & L, const float * x, int64_t xs, int S, void * C, int c_type, int64_t ldc,
                       const float * res, cudaStream_t s);
+    acb_status enqueue_layers(int S, int l0, int l1, cudaStream_t s);
     acb_status enqueue(int S, cudaStream_t s);
     acb_status run(int S, cudaStream_t s);
 };
@@ -148,8 +149,8 @@ acb_status acb_qwen3_enc::linear(const Lin & L, const float * x, int64_t xs, int
                          kPdl | L.op, err.as<int>(), (acb_stream_t) s);
 }
 
-// The whole forward for S tokens whose ids are already in `ids`; result in `out`.
-acb_status acb_qwen3_enc::enqueue(int S, cudaStream_t s) {
+// Layers [l0, l1) over the hidden states in `h` (qwen3_build_layers, qwen3-enc.h:249-262).
+acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) {
     const int    H = c.hidden_size, F = c.intermediate_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
     const int    QD = Nh * D, KD = Nkv * D, NQKV = nqkv();
     const float  eps   = c.rms_norm_eps;
@@ -158,8 +159,8 @@ acb_status acb_qwen3_enc::enqueue(int S, cudaStream_t s) {
     int *        e     = err.as<int>();
     float *      hp    = h.as<float>();
     float *      xp    = xn.as<float>();
-    ACB_TRY(acb_get_rows(embed->data, embed->type, embed->N, H, ids.as<int32_t>(), S, hp, ACB_TYPE_F32, H, e, as));
-    for (const EncLayer & L : layers) {
+    for (int l = l0; l < l1; l++) {
+        const EncLayer & L = layers[(size_t) l];
         ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.attn_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
                              as));
         ACB_TRY(linear(L.qkv, xp, H, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, s));
@@ -179,7 +180,18 @@ acb_status acb_qwen3_enc::enqueue(int S, cudaStream_t s) {
         ACB_TRY(acb_gemm_bf16(xq.p, F, L.down.w, F, S, H, F, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
                               kPdl | L.down.op, e, as));
     }
-    return acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) final_norm->data, out.p, ACB_TYPE_F32, H, S, H, eps, as);
+    return ACB_OK;
+}
+
+// The whole forward for S tokens whose ids are already in `ids`; result in `out`.
+acb_status acb_qwen3_enc::enqueue(int S, cudaStream_t s) {
+    const int          H  = c.hidden_size;
+    const acb_stream_t as = (acb_stream_t) s;
+    ACB_TRY(acb_get_rows(embed->data, embed->type, embed->N, H, ids.as<int32_t>(), S, h.p, ACB_TYPE_F32, H,
+                         err.as<int>(), as));
+    ACB_TRY(enqueue_layers(S, 0, c.n_layers, s));
+    return acb_rms_norm(h.p, ACB_TYPE_F32, H, (const float *) final_norm->data, out.p, ACB_TYPE_F32, H, S, H,
+                        c.rms_norm_eps, as);
 }
 
 // Replay (capturing on first use) the graph for S on stream s.
@@ -412,6 +424,30 @@ extern "C" acb_status acb_qwen3_forward_device(acb_qwen3_enc * m, const int32_t 
     ACB_TRY(m->run(S, s));
     const size_t ob = (size_t) S * m->c.hidden_size * 4;
     return cudaMemcpyAsync(d_out, m->out.p, ob, cudaMemcpyDeviceToDevice, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
+}
+
+extern "C" acb_status acb_qwen3_forward_hidden(acb_qwen3_enc * m, const float * d_hidden, int S, int layer_begin,
+                                               int layer_end, int final_norm, float * d_out, acb_stream_t stream) {
+    if (!m || !d_hidden || !d_out || S <= 0 || layer_begin < 0 || layer_end > m->c.n_layers ||
+        layer_begin > layer_end) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->reserve(S));
+    cudaStream_t s  = (cudaStream_t) stream;
+    const size_t hb = (size_t) S * m->c.hidden_size * 4;
+    if (cudaMemcpyAsync(m->h.p, d_hidden, hb, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->enqueue_layers(S, layer_begin, layer_end, s));
+    if (final_norm) {
+        const int H = m->c.hidden_size;
+        return acb_rms_norm(m->h.p, ACB_TYPE_F32, H, (const float *) m->final_norm->data, d_out, ACB_TYPE_F32, H, S, H,
+                            m->c.rms_norm_eps, stream);
+    }
+    return cudaMemcpyAsync(d_out, m->h.p, hb, cudaMemcpyDeviceToDevice, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
 }
 
 static acb_status check_ids(const acb_qwen3_enc * m, const int32_t * ids, int S) {

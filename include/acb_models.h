@@ -73,6 +73,14 @@ ACB_API acb_status acb_qwen3_forward(acb_qwen3_enc * m, const int32_t * token_id
 ACB_API acb_status acb_qwen3_forward_device(acb_qwen3_enc * m, const int32_t * d_ids, int S, float * d_out,
                                             acb_stream_t stream);
 
+/* qwen3_build_layers (qwen3-enc.h:249-262) over layers [layer_begin, layer_end) from caller
+ * hidden states (device, [S][hidden_size] f32; the condition encoders' entry, cond-enc.h:171,
+ * which start from a projection instead of token ids), positions 0..S-1 and the model's own
+ * masking; d_out receives the resulting hidden states, or their final RMSNorm when final_norm
+ * is nonzero. Enqueued on `stream`, no graph, no host synchronisation. */
+ACB_API acb_status acb_qwen3_forward_hidden(acb_qwen3_enc * m, const float * d_hidden, int S, int layer_begin,
+                                            int layer_end, int final_norm, float * d_out, acb_stream_t stream);
+
 /* qwen3_embed_lookup (qwen3-enc.h:453-480): embedding rows (host ids [S] -> host [S][H] f32). */
 ACB_API acb_status acb_qwen3_embed_lookup(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output);
 ACB_API void       acb_qwen3_free(acb_qwen3_enc * m); /* qwen3_free :483 */

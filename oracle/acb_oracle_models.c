@@ -176,33 +176,42 @@ static int qwen3_layer(const orc_qwen3 * m, const orc_qwen3_layer * ly, float * 
     return rc ? -1 : 0;
 }
 
-int orc_qwen3_encode(const orc_qwen3 * m, const int32_t * ids, int S, float * out) {
-    const int H      = m->H;
-    float *   hidden = fbuf((int64_t) S * H);
-    if (orc_get_rows(m->embed.type, m->embed.data, m->embed.N, H, ids, S, hidden) != 0) {
-        free(hidden);
+int orc_qwen3_layers(const orc_qwen3 * m, float * hidden, int S, int l0, int l1, int causal, float * out) {
+    if (l0 < 0 || l1 > m->n_layers || l0 > l1) {
         return -1;
     }
     int32_t * pos  = (int32_t *) malloc(sizeof(int32_t) * S);
     float *   rope = fbuf((int64_t) S * m->D);
-    float *   mask = fbuf((int64_t) S * S);
+    float *   mask = causal ? fbuf((int64_t) S * S) : NULL;
     for (int i = 0; i < S; i++) {
         pos[i] = i;
-        for (int j = 0; j < S; j++) {
+        for (int j = 0; causal && j < S; j++) {
             mask[(int64_t) i * S + j] = (j <= i) ? 0.0f : -INFINITY;
         }
     }
     orc_rope_cache(rope, pos, S, m->D, m->rope_theta);
     attn_ctx ac = { 0 };
     int      rc = 0;
-    for (int l = 0; l < m->n_layers && rc == 0; l++) {
+    for (int l = l0; l < l1 && rc == 0; l++) {
         rc = qwen3_layer(m, &m->layers[l], hidden, S, rope, &ac, mask);
     }
-    orc_rms_norm(hidden, (const float *) m->final_norm.data, out, S, H, m->eps);
-    free(hidden);
+    if (out) {
+        orc_rms_norm(hidden, (const float *) m->final_norm.data, out, S, m->H, m->eps);
+    }
     free(pos);
     free(rope);
     free(mask);
+    return rc;
+}
+
+int orc_qwen3_encode(const orc_qwen3 * m, const int32_t * ids, int S, float * out) {
+    float * hidden = fbuf((int64_t) S * m->H);
+    if (orc_get_rows(m->embed.type, m->embed.data, m->embed.N, m->H, ids, S, hidden) != 0) {
+        free(hidden);
+        return -1;
+    }
+    const int rc = orc_qwen3_layers(m, hidden, S, 0, m->n_layers, 1, out);
+    free(hidden);
     return rc;
 }
 

@@ -60,6 +60,12 @@ typedef struct {
 /* Text-encoder forward: ids[S] -> out[S][H] (post final norm), causal, f32 attention. */
 int orc_qwen3_encode(const orc_qwen3 * m, const int32_t * ids, int S, float * out);
 
+/* qwen3_build_layers (src/qwen3-enc.h:249-262) over layers [l0, l1) from given hidden states
+ * (in place, [S][H]), positions 0..S-1, causal or unmasked attention; out (optional) receives
+ * the final RMSNorm of the result. The encoder callers that start from a projection
+ * (cond_ggml_forward) and per-layer parity checks use it. */
+int orc_qwen3_layers(const orc_qwen3 * m, float * hidden, int S, int l0, int l1, int causal, float * out);
+
 /* LM prefill of n tokens into kv set `set` starting at position kv_pos; writes the f16 K/V,
  * returns the logits of the last token in logits[V] (or lm rows [lm_offset, lm_offset+lm_count)
  * when lm_count > 0). If hidden_out is non-NULL it receives the final-normed hidden rows

@@ -312,6 +312,8 @@ def _models_lib():
         P, I, F = C.c_void_p, C.c_int, C.c_float
         L.orc_qwen3_encode.restype = I
         L.orc_qwen3_encode.argtypes = [C.POINTER(Qwen3), P, I, P]
+        L.orc_qwen3_layers.restype = I
+        L.orc_qwen3_layers.argtypes = [C.POINTER(Qwen3), P, I, I, I, I, P]
         L.orc_qw3lm_prefill.restype = I
         L.orc_qw3lm_prefill.argtypes = [C.POINTER(Qwen3), C.POINTER(KV), I, I, P, I, P, I, I, P]
         L.orc_qw3lm_decode.restype = I
@@ -346,6 +348,7 @@ class OracleQwen3:
                 qt, raw, K, N = weights[key]
                 setattr(self.layers[i], f[0], tensor(raw, qt, K, N, self.keep))
         qt, raw, K, N = weights["embed"]
+        self.embed_src = (qt, raw, K, N)
         emb = tensor(raw, qt, K, N, self.keep)
         qt, raw, K, N = weights["final_norm"]
         fn = tensor(raw, qt, K, N, self.keep)
@@ -359,6 +362,25 @@ class OracleQwen3:
         rc = _models_lib().orc_qwen3_encode(C.byref(self.m), _p(ids), ids.size, _p(out))
         assert rc == 0
         return out
+
+    def embed_rows(self, ids):
+        """get_rows of the embedding table (the encoder's first hidden states)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        qt, raw, K, _N = self.embed_src
+        rc, out = get_rows(qt, raw, K, ids)
+        assert rc == 0
+        return out
+
+    def layers(self, hidden, l0, l1, causal=True, final_norm=False):
+        """Layers [l0, l1) from hidden [S][H] (returned updated; with final_norm also the normed
+        output): qwen3_build_layers over a layer range."""
+        h = np.array(hidden, dtype=np.float32, copy=True, order="C")
+        S = h.shape[0]
+        out = np.empty_like(h) if final_norm else None
+        rc = _models_lib().orc_qwen3_layers(C.byref(self.m), _p(h), S, l0, l1, int(causal),
+                                            _p(out) if out is not None else None)
+        assert rc == 0
+        return (h, out) if final_norm else h
 
     def alloc_kv(self, n_sets: int, max_seq: int):
         c = self.cfg
