@@ -103,6 +103,9 @@ def lib():
             "acb_act_quant": (I, [P, I64, I64, I64, I, P, I, I64, P]),
             "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
             "acb_vec_dot_type": (I, [I]),
+            "acb_gemm_workspace_bytes": (C.c_size_t, [I64, I64, I64]),
+            "acb_gemm_tc": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, C.c_size_t, P,
+                                P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -361,9 +364,10 @@ class QW3LM:
 # ---- dense path ------------------------------------------------------------------------------------
 
 def gemm_bf16(A, B, out=None, out_dtype=None, bias=None, res=None, gate=None, rows_per_sample=None, flags=0,
-              err=None, stream=None):
+              err=None, stream=None, workspace=None):
     """C = A @ B.T (+ bias) (res + C or res + C * gate) on tcgen05. A [M,K], B [N,K] bf16 (or f16,
-    which sets FLAG_F16) CUDA tensors."""
+    which sets FLAG_F16) CUDA tensors. With `workspace` (a CUDA tensor of at least
+    gemm_workspace_bytes(M, N, K) bytes) small-M shapes split K (acb_gemm_tc)."""
     import torch
     if A.dtype == torch.float16:
         flags |= FLAG_F16
@@ -372,11 +376,16 @@ def gemm_bf16(A, B, out=None, out_dtype=None, bias=None, res=None, gate=None, ro
     if out is None:
         out = torch.empty((M, N), dtype=out_dtype or torch.float32, device=A.device)
     gs = 0 if gate is None else (gate.stride(0) if gate.dim() > 1 else 0)
-    _check("acb_gemm_bf16", lib().acb_gemm_bf16(
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check("acb_gemm_tc", lib().acb_gemm_tc(
         _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, N, K, _ptr(out), dtype_id(out), out.stride(0), _ptr(bias),
-        _ptr(res), res.stride(0) if res is not None else 0, _ptr(gate), gs, rows_per_sample or M, flags, _ptr(err),
-        _stream(stream)))
+        _ptr(res), res.stride(0) if res is not None else 0, _ptr(gate), gs, rows_per_sample or M, flags,
+        _ptr(workspace), wsb, _ptr(err), _stream(stream)))
     return out
+
+
+def gemm_workspace_bytes(M, N, K) -> int:
+    return lib().acb_gemm_workspace_bytes(M, N, K)
 
 
 MASK_NONE, MASK_CAUSAL, MASK_WINDOW = 0, 1, 2

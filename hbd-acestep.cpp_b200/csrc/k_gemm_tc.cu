@@ -44,6 +44,9 @@ struct GemmArgs {
     int64_t       gate_stride;
     int64_t       rows_per_sample;
     int *         err;
+    int           splits;  // split-K factor; > 1: raw partials to ws, epilogue by splitk_reduce_kernel
+    int           kps;     // k-tiles per split
+    float *       ws;      // [splits][M][N] f32 partial accumulators
 };
 
 // ---- tcgen05 / TMA helpers ------------------------------------------------------------------------
@@ -150,7 +153,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t m_tiles = (g.M + kBM - 1) / kBM, n_tiles = (g.N + kBN - 1) / kBN;
-    const int64_t n_work  = m_tiles * n_tiles;
+    const int64_t tiles   = m_tiles * n_tiles;
+    const int64_t n_work  = tiles * g.splits;
     const int     k_tiles = (int) (g.K / kBK);
 
     if (threadIdx.x == 0) {
@@ -183,8 +187,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {
             int it = 0;  // global k-stage counter
             for (int64_t w = blockIdx.x; w < n_work && !abort_flag; w += gridDim.x) {
-                const int m0 = (int) ((w % m_tiles) * kBM), n0 = (int) ((w / m_tiles) * kBN);
-                for (int kt = 0; kt < k_tiles; kt++, it++) {
+                const int64_t t  = w % tiles;
+                const int     sp = (int) (w / tiles);
+                const int m0 = (int) ((t % m_tiles) * kBM), n0 = (int) ((t / m_tiles) * kBN);
+                const int kt1 = min(k_tiles, (sp + 1) * g.kps);
+                for (int kt = sp * g.kps; kt < kt1; kt++, it++) {
                     const int s = it % kStages;
                     if (it >= kStages && !ptx::mbar_wait(&empty[s], ((it / kStages) - 1) & 1)) {
                         flag_timeout(g.err);
@@ -212,7 +219,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + (uint32_t) (acc * kBN);
-                for (int kt = 0; kt < k_tiles; kt++, it++) {
+                const int      kt0    = (int) (w / tiles) * g.kps;
+                const int      kt1    = min(k_tiles, kt0 + g.kps);
+                for (int kt = kt0; kt < kt1; kt++, it++) {
                     const int s = it % kStages;
                     if (!ptx::mbar_wait(&full[s], (it / kStages) & 1)) {
                         flag_timeout(g.err);
@@ -225,7 +234,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; kk++) {
                         umma_f16kind(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                                  (kt | kk) != 0 ? 1u : 0u);
+                                  (kt != kt0 || kk != 0) ? 1u : 0u);
                     }
                     umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
                 }
@@ -247,10 +256,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t m = (w % m_tiles) * kBM + row_in_tile;
-            const int64_t n0 = (w / m_tiles) * kBN;
-            const float * gate_row =
-                (g.epi & EPI_GATED_RES) ? g.gate + (m < g.M ? (m / g.rows_per_sample) : 0) * g.gate_stride : nullptr;
+            const int64_t t  = w % tiles;
+            const int64_t m  = (t % m_tiles) * kBM + row_in_tile;
+            const int64_t n0 = (t / m_tiles) * kBN;
+            const bool    part = g.splits > 1;  // raw partial of split w / tiles
+            float *       pdst = part ? g.ws + ((w / tiles) * g.M + m) * g.N : nullptr;
+            const float * gate_row = (!part && (g.epi & EPI_GATED_RES))
+                                         ? g.gate + (m < g.M ? (m / g.rows_per_sample) : 0) * g.gate_stride
+                                         : nullptr;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; c++) {
                 uint32_t r[32];
@@ -263,6 +276,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     v[j] = __uint_as_float(r[j]);
                 }
                 const bool full_cols = nc + 32 <= g.N;
+                if (part) {
+                    float * dst = pdst + nc;
+                    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        }
+                    } else {
+                        for (int j = 0; j < 32 && nc + j < g.N; j++) {
+                            dst[j] = v[j];
+                        }
+                    }
+                } else {  // final tile: epilogue and store
                 if (g.bias) {
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
@@ -298,6 +324,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 } else {
                     store_row16<ACB_TYPE_F16>(g.C, m * g.ldc + nc, v, full_cols, (int) (g.N - nc));
                 }
+                }  // final tile
                 }  // valid row and column chunk
             }
             tc_fence_before();
@@ -314,6 +341,78 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
     }
+}
+
+// Split-K second pass: C = epilogue(sum over splits of the partials, in split order), four
+// consecutive columns per thread. Deterministic: every element is summed in the same order.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs g) {
+    ptx::grid_dep_wait();
+    const int64_t nq  = g.N / 4;
+    const int64_t idx = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx < g.M * nq) {
+        const int64_t m = idx / nq, n = (idx - m * nq) * 4;
+        float4        a = *reinterpret_cast<const float4 *>(g.ws + m * g.N + n);
+        float         v[4] = { a.x, a.y, a.z, a.w };
+        for (int sp = 1; sp < g.splits; sp++) {
+            const float4 b = *reinterpret_cast<const float4 *>(g.ws + (sp * g.M + m) * g.N + n);
+            v[0] = __fadd_rn(v[0], b.x);
+            v[1] = __fadd_rn(v[1], b.y);
+            v[2] = __fadd_rn(v[2], b.z);
+            v[3] = __fadd_rn(v[3], b.w);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (g.bias) {
+                v[j] = __fadd_rn(v[j], g.bias[n + j]);
+            }
+            if (g.epi & (EPI_RES | EPI_GATED_RES)) {
+                const float o = (g.epi & EPI_GATED_RES)
+                                    ? __fmul_rn(v[j], g.gate[(m / g.rows_per_sample) * g.gate_stride + n + j])
+                                    : v[j];
+                v[j] = __fadd_rn(g.res[m * g.ldr + n + j], o);
+            }
+        }
+        if (g.c_type == ACB_TYPE_F32) {
+            float * d = reinterpret_cast<float *>(g.C) + m * g.ldc + n;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                d[j] = v[j];
+            }
+        } else if (g.c_type == ACB_TYPE_BF16) {
+            __nv_bfloat16 * d = reinterpret_cast<__nv_bfloat16 *>(g.C) + m * g.ldc + n;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                d[j] = __float2bfloat16_rn(v[j]);
+            }
+        } else {
+            __half * d = reinterpret_cast<__half *>(g.C) + m * g.ldc + n;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                d[j] = __float2half_rn(v[j]);
+            }
+        }
+    }
+    ptx::grid_dep_launch();
+}
+
+// Split-K factor for an M x N x K GEMM: only when the output tiles leave most SMs idle; every
+// split keeps at least 4 k-tiles (256 of K) so its pipeline fill stays amortised.
+static int choose_splits(int64_t M, int64_t N, int64_t K, int * kps) {
+    const int64_t tiles   = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int     k_tiles = (int) (K / kBK);
+    const int     sms     = num_sms();
+    *kps                  = k_tiles;
+    if (tiles * 2 > sms || k_tiles < 8 || N % 4 != 0) {
+        return 1;
+    }
+    int sp = (int) (sms / tiles);
+    sp     = sp < k_tiles / 4 ? sp : k_tiles / 4;
+    sp     = sp < 16 ? sp : 16;
+    if (sp < 2) {
+        return 1;
+    }
+    *kps = (k_tiles + sp - 1) / sp;
+    return (k_tiles + *kps - 1) / *kps;
 }
 
 // ---- host: tensor maps through the driver entry point (no libcuda link) ----------------------------
@@ -355,10 +454,20 @@ static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K
 
 using namespace acb;
 
-extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
-                                    int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
-                                    int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
-                                    int flags, int * err_flag, acb_stream_t stream) {
+extern "C" size_t acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0) {
+        return 0;
+    }
+    int       kps = 0;
+    const int sp  = choose_splits(M, N, K, &kps);
+    return sp > 1 ? (size_t) sp * (size_t) M * (size_t) N * 4 : 0;
+}
+
+extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
+                                  int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
+                                  int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
+                                  int flags, void * workspace, size_t workspace_bytes, int * err_flag,
+                                  acb_stream_t stream) {
     if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || lda < K || ldb < K || ldc < N) {
         return ACB_ERR_INVALID_ARG;
     }
@@ -387,12 +496,24 @@ extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B,
     g.gate_stride     = gate_stride;
     g.rows_per_sample = rows_per_sample > 0 ? rows_per_sample : 1;
     g.err             = err_flag;
+    g.splits          = 1;
+    g.kps             = (int) (K / kBK);
+    {
+        int       kps = 0;
+        const int sp  = choose_splits(M, N, K, &kps);
+        if (sp > 1 && workspace && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 &&
+            workspace_bytes >= (size_t) sp * (size_t) M * (size_t) N * 4) {
+            g.splits = sp;
+            g.kps    = kps;
+            g.ws     = reinterpret_cast<float *>(workspace);
+        }
+    }
+    const bool  f16 = (flags & ACB_FLAG_F16) != 0;
     CUtensorMap ta, tb;
-    const bool f16 = (flags & ACB_FLAG_F16) != 0;
     if (!make_map(&ta, A, M, K, lda, kBM, f16) || !make_map(&tb, B, N, K, ldb, kBN, f16)) {
         return ACB_ERR_CUDA;
     }
-    const int64_t work = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int64_t work = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * g.splits;
     const int     grid = (int) (work < num_sms() ? work : num_sms());
     const size_t  smem = (size_t) kStages * kStageBytes + 1024 + 256;
     void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
@@ -406,12 +527,30 @@ extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B,
     cudaLaunchAttribute attr[1];
     attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs                                          = (flags & 1) ? attr : nullptr;
-    cfg.numAttrs                                       = (flags & 1) ? 1 : 0;
-    const cudaError_t e                                = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+    cfg.attrs                                          = (flags & ACB_FLAG_PDL) ? attr : nullptr;
+    cfg.numAttrs                                       = (flags & ACB_FLAG_PDL) ? 1 : 0;
+    cudaError_t e                                      = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+    if (e == cudaSuccess && g.splits > 1) {
+        // the reduction always waits on the GEMM through griddepcontrol.wait
+        const int64_t n_thr = M * (N / 4);
+        cfg.gridDim         = dim3((unsigned) ((n_thr + 255) / 256));
+        cfg.blockDim        = dim3(256);
+        cfg.dynamicSmemBytes = 0;
+        cfg.attrs           = attr;
+        cfg.numAttrs        = 1;
+        e                   = cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, g);
+    }
     if (e != cudaSuccess) {
         set_last_cuda_error(e);
         return ACB_ERR_CUDA;
     }
     return ACB_OK;
+}
+
+extern "C" acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
+                                    int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
+                                    int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
+                                    int flags, int * err_flag, acb_stream_t stream) {
+    return acb_gemm_tc(A, lda, B, ldb, M, N, K, C, c_type, ldc, bias, res, ldr, gate, gate_stride, rows_per_sample,
+                       flags, nullptr, 0, err_flag, stream);
 }

@@ -68,7 +68,7 @@ struct acb_qwen3_enc {
 
     // scratch for up to cap tokens
     int                            cap = 0;
-    DevBuf                         ids, pos, rope, h, xn, xq, qkv, q, k, att, gu, out, err;
+    DevBuf                         ids, pos, rope, h, xn, xq, qkv, q, k, att, gu, out, err, ws;
     std::map<int, cudaGraphExec_t> graphs;  // one per S
 
     ~acb_qwen3_enc() {
@@ -118,6 +118,16 @@ acb_status acb_qwen3_enc::reserve(int S) {
     bad |= gu.alloc((size_t) n * 2 * F * 4) != ACB_OK;
     bad |= out.alloc((size_t) n * H * 4) != ACB_OK;
     bad |= rope.alloc((size_t) n * c.head_dim * 4, false) != ACB_OK;
+    {
+        // split-K workspace: the largest need over the four linears at every M tile count <= n
+        size_t wsb = 0;
+        for (int m = 128; m < n + 128; m += 128) {
+            const int64_t M = std::min(m, n);
+            wsb = std::max({ wsb, acb_gemm_workspace_bytes(M, nqkv(), H), acb_gemm_workspace_bytes(M, H, QD),
+                             acb_gemm_workspace_bytes(M, 2 * F, H), acb_gemm_workspace_bytes(M, H, F) });
+        }
+        bad |= ws.alloc(wsb, false) != ACB_OK;
+    }
     if (!err.p) {
         bad |= err.alloc(4) != ACB_OK;
     }
@@ -145,8 +155,8 @@ acb_status acb_qwen3_enc::reserve(int S) {
 acb_status acb_qwen3_enc::linear(const Lin & L, const float * x, int64_t xs, int S, void * C, int c_type,
                                  int64_t ldc, const float * res, cudaStream_t s) {
     ACB_TRY(acb_act_quant(x, xs, S, L.K, L.vec, xq.p, L.act_type(), L.K, (acb_stream_t) s));
-    return acb_gemm_bf16(xq.p, L.K, L.w, L.K, S, L.N, L.K, C, c_type, ldc, nullptr, res, res ? ldc : 0, nullptr, 0, 0,
-                         kPdl | L.op, err.as<int>(), (acb_stream_t) s);
+    return acb_gemm_tc(xq.p, L.K, L.w, L.K, S, L.N, L.K, C, c_type, ldc, nullptr, res, res ? ldc : 0, nullptr, 0, 0,
+                       kPdl | L.op, ws.p, ws.bytes, err.as<int>(), (acb_stream_t) s);
 }
 
 // Layers [l0, l1) over the hidden states in `h` (qwen3_build_layers, qwen3-enc.h:249-262).
@@ -177,8 +187,8 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
                              as));
         ACB_TRY(linear(L.gu, xp, H, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, s));
         ACB_TRY(acb_act_quant_swiglu(gu.as<float>(), 2 * F, F, S, F, L.down.vec, xq.p, L.down.act_type(), F, as));
-        ACB_TRY(acb_gemm_bf16(xq.p, F, L.down.w, F, S, H, F, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
-                              kPdl | L.down.op, e, as));
+        ACB_TRY(acb_gemm_tc(xq.p, F, L.down.w, F, S, H, F, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
+                            kPdl | L.down.op, ws.p, ws.bytes, e, as));
     }
     return ACB_OK;
 }

@@ -184,6 +184,19 @@ ACB_API acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, in
                                  int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
                                  int flags, int * err_flag, acb_stream_t stream);
 
+/* acb_gemm_bf16 with a split-K workspace: when the output tiles of an M x N GEMM would leave
+ * most SMs idle (few tokens, e.g. the text encoder's 256), K is split across CTAs that write f32
+ * partial tiles to `workspace` ([splits][M][N], 16-byte aligned), and a second kernel sums them
+ * in split order (deterministic) and applies the epilogue. acb_gemm_workspace_bytes gives the
+ * bytes needed at these sizes (0: no split is used); a smaller or NULL workspace runs unsplit.
+ * Calls sharing one workspace must not overlap. */
+ACB_API size_t     acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+ACB_API acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
+                               int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
+                               int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
+                               int flags, void * workspace, size_t workspace_bytes, int * err_flag,
+                               acb_stream_t stream);
+
 /* Attention over whole sequences (flash tiling on tensor cores, fp32 softmax and
  * accumulation), head_dim 128, GQA head h -> kv head h / (Nh/Nkv):
  *   O[b,i,h] = softmax_j(Q[b,i,h].K[b,j,h'] * scale + mask) V[b,j,h']

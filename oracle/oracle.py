@@ -371,7 +371,7 @@ class OracleQwen3:
         assert rc == 0
         return out
 
-    def layers(self, hidden, l0, l1, causal=True, final_norm=False):
+    def run_layers(self, hidden, l0, l1, causal=True, final_norm=False):
         """Layers [l0, l1) from hidden [S][H] (returned updated; with final_norm also the normed
         output): qwen3_build_layers over a layer range."""
         h = np.array(hidden, dtype=np.float32, copy=True, order="C")

@@ -56,7 +56,7 @@ def _check_per_layer(enc, om, ids, cfg, cuda):
     h = om.embed_rows(ids)
     worst = (1.0, 0.0)
     for l in range(cfg["num_hidden_layers"]):
-        want = om.layers(h, l, l + 1)
+        want = om.run_layers(h, l, l + 1)
         got = enc.forward_hidden(torch.from_numpy(h).to(cuda), l, l + 1).cpu().numpy()
         cs, mr = _check_rows(got, want, f"layer {l}")
         worst = (min(worst[0], cs), max(worst[1], mr))
