@@ -99,6 +99,10 @@ def lib():
             "acb_qwen3_forward_device": (I, [P, P, I, P, P]),
             "acb_qwen3_embed_lookup": (I, [P, P, I, P]),
             "acb_qwen3_forward_hidden": (I, [P, P, I, I, I, I, P, P]),
+            "acb_qwen3_set_exact": (I, [P, I]),
+            "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
+            "acb_attn_prefill_split": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I,
+                                           I, I, F, I, I64, I64, I64, P]),
             "acb_qwen3_free": (None, [P]),
             "acb_act_quant": (I, [P, I64, I64, I64, I, P, I, I64, P]),
             "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
@@ -473,6 +477,10 @@ class Qwen3Encoder:
     def weight_bytes(self) -> int:
         return lib().acb_qwen3_weight_bytes(self.h)
 
+    def set_exact(self, exact: bool):
+        """exact (default): hi/lo split products tracking the reference to fp32 order; fast: f16."""
+        _check("acb_qwen3_set_exact", lib().acb_qwen3_set_exact(self.h, int(bool(exact))))
+
     def forward(self, ids):
         """Host ids [S] -> host hidden states [S][H] f32 (final RMSNorm applied)."""
         ids = self.np.ascontiguousarray(ids, dtype=self.np.int32)
@@ -502,3 +510,38 @@ class Qwen3Encoder:
         _check("acb_qwen3_embed_lookup", lib().acb_qwen3_embed_lookup(self.h, ids.ctypes.data, ids.size,
                                                                       out.ctypes.data))
         return out
+
+
+LAYOUT_PLAIN, LAYOUT_GEMM_A, LAYOUT_GEMM_B, LAYOUT_PLANES = 0, 1, 2, 3
+
+
+def act_quant_ex(x, K, vec_type, layout, up_offset=0, out=None, lo_offset=0, stream=None):
+    """acb_act_quant_ex over x [M, >=K] f32 (up_offset > 0: SwiGLU rows)."""
+    import torch
+    M = x.shape[0]
+    dt = torch.bfloat16 if vec_type == BF16 else torch.float16
+    width = 3 * K if layout in (LAYOUT_GEMM_A, LAYOUT_GEMM_B) else K
+    if out is None:
+        out = torch.empty((2 * M if layout == LAYOUT_PLANES else M, width), dtype=dt, device=x.device)
+        if layout == LAYOUT_PLANES:
+            lo_offset = M * width
+    _check("acb_act_quant_ex", lib().acb_act_quant_ex(_ptr(x), x.stride(0), up_offset, M, K, vec_type, layout,
+                                                      _ptr(out), dtype_id(out), width, lo_offset, _stream(stream)))
+    return out
+
+
+def attn_prefill_split(q, k, v, q_lo, k_lo, v_lo, Nh, Nkv, mask=MASK_NONE, window=0, causal_off=0, out=None,
+                       scale=None, flags=0, stream=None):
+    """Split-precision attention: q/k/v f16 hi-plane views, *_lo the element offsets of the lo planes."""
+    import math
+
+    import torch
+    B, Sq = q.shape[0], q.shape[1]
+    Skv = k.shape[1]
+    if out is None:
+        out = torch.empty((B, Sq, Nh * 128), dtype=torch.float32, device=q.device)
+    _check("acb_attn_prefill_split", lib().acb_attn_prefill_split(
+        _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0), v.stride(1),
+        _ptr(out), dtype_id(out), out.stride(0), out.stride(1), B, Sq, Skv, Nh, Nkv, 128, mask, window, causal_off,
+        scale if scale is not None else 1.0 / math.sqrt(128), flags, q_lo, k_lo, v_lo, _stream(stream)))
+    return out

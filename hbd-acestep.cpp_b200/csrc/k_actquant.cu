@@ -29,10 +29,33 @@ __device__ __forceinline__ void load8(const float * p, bool vec, float * v) {
     }
 }
 
-template <int VT, bool SWIGLU>
+// 8 values of a lane as 16-bit operands at dst (vector store when allowed)
+template <int OT> __device__ __forceinline__ void store8(void * dst, const float * o, bool vec) {
+    using et = typename io<OT>::t;
+    et * yr  = reinterpret_cast<et *>(dst);
+    if (vec) {
+        vec16<OT> pk;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            pk.v[e] = io<OT>::from_f(o[e]);
+        }
+        *reinterpret_cast<uint4 *>(yr) = pk.u;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            yr[e] = io<OT>::from_f(o[e]);
+        }
+    }
+}
+
+template <int OT, int LAYOUT>
+__device__ __forceinline__ void split_store(typename io<OT>::t * yr, const float * o, int64_t K, int64_t lo_off,
+                                            bool vec_out);
+
+template <int VT, bool SWIGLU, int LAYOUT>
 __global__ void __launch_bounds__(kAqWarps * 32)
     act_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t up_off, int64_t rows, int64_t K,
-                     void * __restrict__ y, int64_t ys, bool vec_in, bool vec_out) {
+                     void * __restrict__ y, int64_t ys, int64_t lo_off, bool vec_in, bool vec_out) {
     const int     lane   = threadIdx.x & 31;
     const int64_t chunks = (K + 255) / 256;
     const int64_t item   = (int64_t) blockIdx.x * kAqWarps + (threadIdx.x >> 5);
@@ -125,21 +148,38 @@ __global__ void __launch_bounds__(kAqWarps * 32)
     if (!valid) {
         return;
     }
-    using et = typename io<VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16>::t;
     constexpr int OT = VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
-    et * yr = reinterpret_cast<et *>(y) + r * ys + c0;
-    if (vec_out) {
-        vec16<OT> pk;
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            pk.v[e] = io<OT>::from_f(o[e]);
-        }
-        *reinterpret_cast<uint4 *>(yr) = pk.u;
+    using et         = typename io<OT>::t;
+    et * yr          = reinterpret_cast<et *>(y) + r * ys + c0;
+    if constexpr (LAYOUT == ACB_LAYOUT_PLAIN) {
+        store8<OT>(yr, o, vec_out);
     } else {
+        split_store<OT, LAYOUT>(yr, o, K, lo_off, vec_out);
+    }
+}
+
+template <int OT, int LAYOUT>
+__device__ __forceinline__ void split_store(typename io<OT>::t * yr, const float * o, int64_t K, int64_t lo_off,
+                                            bool vec_out) {
+    // exact split: hi = f16(v), lo = f16(v - hi); v - hi is exact in f32, and for values of at
+    // most 22 significant bits (every dequantised operand here has <= 18) hi + lo == v exactly
+    float hi[8], lo[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            yr[e] = io<OT>::from_f(o[e]);
-        }
+    for (int e = 0; e < 8; e++) {
+        hi[e] = io<OT>::to_f(io<OT>::from_f(o[e]));
+        lo[e] = __fsub_rn(o[e], hi[e]);
+    }
+    if (LAYOUT == ACB_LAYOUT_GEMM_A) {  // [hi | hi | lo] along K
+        store8<OT>(yr, hi, vec_out);
+        store8<OT>(yr + K, hi, vec_out);
+        store8<OT>(yr + 2 * K, lo, vec_out);
+    } else if (LAYOUT == ACB_LAYOUT_GEMM_B) {  // [hi | lo | hi] along K
+        store8<OT>(yr, hi, vec_out);
+        store8<OT>(yr + K, lo, vec_out);
+        store8<OT>(yr + 2 * K, hi, vec_out);
+    } else {  // ACB_LAYOUT_PLANES: hi here, lo at lo_off elements further
+        store8<OT>(yr, hi, vec_out);
+        store8<OT>(yr + lo_off, lo, vec_out);
     }
 }
 
@@ -163,40 +203,66 @@ extern "C" int acb_vec_dot_type(int weight_type) {
     }
 }
 
+template <int VT, bool SWIGLU>
+static void launch_layout(int layout, dim3 grid, cudaStream_t st, const float * x, int64_t xs, int64_t up_off,
+                          int64_t rows, int64_t K, void * y, int64_t ys, int64_t lo_off, bool vin, bool vout) {
+#define ACB_AQL(L) \
+    act_quant_kernel<VT, SWIGLU, L><<<grid, kAqWarps * 32, 0, st>>>(x, xs, up_off, rows, K, y, ys, lo_off, vin, vout)
+    switch (layout) {
+        case ACB_LAYOUT_GEMM_A:
+            ACB_AQL(ACB_LAYOUT_GEMM_A);
+            break;
+        case ACB_LAYOUT_GEMM_B:
+            ACB_AQL(ACB_LAYOUT_GEMM_B);
+            break;
+        case ACB_LAYOUT_PLANES:
+            ACB_AQL(ACB_LAYOUT_PLANES);
+            break;
+        default:
+            ACB_AQL(ACB_LAYOUT_PLAIN);
+    }
+#undef ACB_AQL
+}
+
 template <bool SWIGLU>
 static acb_status launch_act_quant(const float * x, int64_t x_stride, int64_t up_off, int64_t rows, int64_t K,
-                                   int vec_type, void * y, int y_type, int64_t y_stride, cudaStream_t st) {
+                                   int vec_type, int layout, void * y, int y_type, int64_t y_stride, int64_t lo_off,
+                                   cudaStream_t st) {
     const int want_y = vec_type == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
-    if (y_type != want_y || K % 32 != 0 || (vec_type == ACB_TYPE_Q8_K && K % 256 != 0)) {
+    if (y_type != want_y || K % 32 != 0 || (vec_type == ACB_TYPE_Q8_K && K % 256 != 0) || layout < 0 || layout > 3) {
         return ACB_ERR_UNSUPPORTED;
+    }
+    if ((layout == ACB_LAYOUT_GEMM_A || layout == ACB_LAYOUT_GEMM_B) && y_stride < 3 * K) {
+        return ACB_ERR_INVALID_ARG;
     }
     if (rows == 0) {
         return ACB_OK;
     }
-    const bool vin = (x_stride % 4 == 0) && (up_off % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-    const bool vout = (y_stride % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    const bool vin  = (x_stride % 4 == 0) && (up_off % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    const bool vout = (y_stride % 8 == 0) && (K % 8 == 0) && (lo_off % 8 == 0) &&
+                      (reinterpret_cast<uintptr_t>(y) % 16 == 0);
     const int64_t items = rows * ((K + 255) / 256);
     const dim3    grid((unsigned) ((items + kAqWarps - 1) / kAqWarps));
-#define ACB_AQ(VT)                                                                                              \
-    act_quant_kernel<VT, SWIGLU><<<grid, kAqWarps * 32, 0, st>>>(x, x_stride, up_off, rows, K, y, y_stride, vin, \
-                                                                 vout)
     switch (vec_type) {
         case ACB_TYPE_Q8_0:
-            ACB_AQ(ACB_TYPE_Q8_0);
+            launch_layout<ACB_TYPE_Q8_0, SWIGLU>(layout, grid, st, x, x_stride, up_off, rows, K, y, y_stride, lo_off,
+                                                 vin, vout);
             break;
         case ACB_TYPE_Q8_K:
-            ACB_AQ(ACB_TYPE_Q8_K);
+            launch_layout<ACB_TYPE_Q8_K, SWIGLU>(layout, grid, st, x, x_stride, up_off, rows, K, y, y_stride, lo_off,
+                                                 vin, vout);
             break;
         case ACB_TYPE_F16:
-            ACB_AQ(ACB_TYPE_F16);
+            launch_layout<ACB_TYPE_F16, SWIGLU>(layout, grid, st, x, x_stride, up_off, rows, K, y, y_stride, lo_off,
+                                                vin, vout);
             break;
         case ACB_TYPE_BF16:
-            ACB_AQ(ACB_TYPE_BF16);
+            launch_layout<ACB_TYPE_BF16, SWIGLU>(layout, grid, st, x, x_stride, up_off, rows, K, y, y_stride, lo_off,
+                                                 vin, vout);
             break;
         default:
             return ACB_ERR_UNSUPPORTED;
     }
-#undef ACB_AQ
     return launch_status();
 }
 
@@ -205,7 +271,8 @@ extern "C" acb_status acb_act_quant(const float * x, int64_t x_stride, int64_t r
     if (!x || !y || rows < 0 || K <= 0 || x_stride < K || y_stride < K) {
         return ACB_ERR_INVALID_ARG;
     }
-    return launch_act_quant<false>(x, x_stride, 0, rows, K, vec_type, y, y_type, y_stride, (cudaStream_t) stream);
+    return launch_act_quant<false>(x, x_stride, 0, rows, K, vec_type, ACB_LAYOUT_PLAIN, y, y_type, y_stride, 0,
+                                   (cudaStream_t) stream);
 }
 
 extern "C" acb_status acb_act_quant_swiglu(const float * gu, int64_t gu_stride, int64_t up_offset, int64_t rows,
@@ -214,6 +281,24 @@ extern "C" acb_status acb_act_quant_swiglu(const float * gu, int64_t gu_stride, 
     if (!gu || !y || rows < 0 || F <= 0 || up_offset < F || gu_stride < up_offset + F || y_stride < F) {
         return ACB_ERR_INVALID_ARG;
     }
-    return launch_act_quant<true>(gu, gu_stride, up_offset, rows, F, vec_type, y, y_type, y_stride,
-                                  (cudaStream_t) stream);
+    return launch_act_quant<true>(gu, gu_stride, up_offset, rows, F, vec_type, ACB_LAYOUT_PLAIN, y, y_type, y_stride,
+                                  0, (cudaStream_t) stream);
+}
+
+extern "C" acb_status acb_act_quant_ex(const float * x, int64_t x_stride, int64_t up_offset, int64_t rows, int64_t K,
+                                       int vec_type, int layout, void * y, int y_type, int64_t y_stride,
+                                       int64_t lo_offset, acb_stream_t stream) {
+    if (!x || !y || rows < 0 || K <= 0 || y_stride < K || up_offset < 0 ||
+        (up_offset > 0 && (up_offset < K || x_stride < up_offset + K)) || (up_offset == 0 && x_stride < K)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (layout == ACB_LAYOUT_PLANES && lo_offset == 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (up_offset > 0) {
+        return launch_act_quant<true>(x, x_stride, up_offset, rows, K, vec_type, layout, y, y_type, y_stride,
+                                      lo_offset, (cudaStream_t) stream);
+    }
+    return launch_act_quant<false>(x, x_stride, 0, rows, K, vec_type, layout, y, y_type, y_stride, lo_offset,
+                                   (cudaStream_t) stream);
 }

@@ -35,6 +35,7 @@ struct AttnArgs {
     int                   window;      // MASK_WINDOW: |i - j| <= window
     int                   causal_off;  // MASK_CAUSAL: key j allowed when j <= i + causal_off
     float                 scale_log2;  // scale * log2(e)
+    int64_t               q_lo, k_lo, v_lo;  // SPLIT: element offsets of the lo planes
 };
 
 __device__ __forceinline__ void cp_async16(void * dst, const void * src, bool pred) {
@@ -99,12 +100,19 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16 * sm, const __nv_bfloat1
     }
 }
 
-template <int MASK, bool F16>
+// SPLIT: every operand is given as f16 hi and lo planes (hi + lo == the f32 value) and each
+// product is formed as hi.hi + hi.lo + lo.hi, which reproduces f32 attention to ~2^-22; the
+// probabilities are split the same way before P.V.
+template <int MASK, bool F16, bool SPLIT>
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
+    constexpr int   kTile = kAttnBQ * kAttnPad;        // elements per padded 64-row tile
     __nv_bfloat16 * sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
-    __nv_bfloat16 * sK = sQ + kAttnBQ * kAttnPad;       // 2 buffers
-    __nv_bfloat16 * sV = sK + 2 * kAttnBK * kAttnPad;   // 2 buffers
+    __nv_bfloat16 * sK = sQ + kTile;                   // 2 buffers
+    __nv_bfloat16 * sV = sK + 2 * kTile;               // 2 buffers
+    __nv_bfloat16 * sQl = sV + 2 * kTile;              // SPLIT only: lo planes
+    __nv_bfloat16 * sKl = sQl + kTile;
+    __nv_bfloat16 * sVl = sKl + 2 * kTile;
 
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -127,9 +135,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
     }
 
     load_tile(sQ, Qg + (int64_t) 0, a.q_ts, q0, a.Sq);
+    if (SPLIT) {
+        load_tile(sQl, Qg + a.q_lo, a.q_ts, q0, a.Sq);
+    }
     if (kb_lo < kb_hi) {
         load_tile(sK, Kg, a.k_ts, kb_lo * kAttnBK, a.Skv);
         load_tile(sV, Vg, a.v_ts, kb_lo * kAttnBK, a.Skv);
+        if (SPLIT) {
+            load_tile(sKl, Kg + a.k_lo, a.k_ts, kb_lo * kAttnBK, a.Skv);
+            load_tile(sVl, Vg + a.v_lo, a.v_ts, kb_lo * kAttnBK, a.Skv);
+        }
     }
     cp_async_commit();
 
@@ -150,19 +165,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
         if (kb + 1 < kb_hi) {
             load_tile(sK + (buf ^ 1) * kAttnBK * kAttnPad, Kg, a.k_ts, (kb + 1) * kAttnBK, a.Skv);
             load_tile(sV + (buf ^ 1) * kAttnBK * kAttnPad, Vg, a.v_ts, (kb + 1) * kAttnBK, a.Skv);
+            if (SPLIT) {
+                load_tile(sKl + (buf ^ 1) * kAttnBK * kAttnPad, Kg + a.k_lo, a.k_ts, (kb + 1) * kAttnBK, a.Skv);
+                load_tile(sVl + (buf ^ 1) * kAttnBK * kAttnPad, Vg + a.v_lo, a.v_ts, (kb + 1) * kAttnBK, a.Skv);
+            }
         }
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        if (kb == kb_lo) {
+        if (!SPLIT && kb == kb_lo) {
 #pragma unroll
             for (int ks = 0; ks < 8; ks++) {
                 const __nv_bfloat16 * p = sQ + (warp * 16 + (lane & 15)) * kAttnPad + ks * 16 + (lane >> 4) * 8;
                 ldsm_x4(qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], p);
             }
         }
-        const __nv_bfloat16 * Kb = sK + buf * kAttnBK * kAttnPad;
-        const __nv_bfloat16 * Vb = sV + buf * kAttnBK * kAttnPad;
+        const __nv_bfloat16 * Kb  = sK + buf * kAttnBK * kAttnPad;
+        const __nv_bfloat16 * Vb  = sV + buf * kAttnBK * kAttnPad;
+        const __nv_bfloat16 * Kbl = sKl + buf * kAttnBK * kAttnPad;
+        const __nv_bfloat16 * Vbl = sVl + buf * kAttnBK * kAttnPad;
 
         // S = Q K^T for 16 rows x 64 keys
         float s[8][4];
@@ -175,14 +196,31 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
         }
 #pragma unroll
         for (int ks = 0; ks < 8; ks++) {
+            uint32_t qh[4], ql[4];
+            if (SPLIT) {  // Q fragments re-read per key block (registers go to the split products)
+                const int off = (warp * 16 + (lane & 15)) * kAttnPad + ks * 16 + (lane >> 4) * 8;
+                ldsm_x4(qh[0], qh[1], qh[2], qh[3], sQ + off);
+                ldsm_x4(ql[0], ql[1], ql[2], ql[3], sQl + off);
+            }
 #pragma unroll
             for (int np = 0; np < 4; np++) {  // pairs of 8-key n-tiles
                 uint32_t b0, b1, b2, b3;
                 const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
                 const int d   = ks * 16 + ((lane >> 3) & 1) * 8;
                 ldsm_x4(b0, b1, b2, b3, Kb + key * kAttnPad + d);
-                mma16<F16>(s[2 * np], qf[ks], b0, b1);
-                mma16<F16>(s[2 * np + 1], qf[ks], b2, b3);
+                if (SPLIT) {
+                    uint32_t c0, c1, c2, c3;
+                    ldsm_x4(c0, c1, c2, c3, Kbl + key * kAttnPad + d);
+                    mma16<F16>(s[2 * np], ql, b0, b1);
+                    mma16<F16>(s[2 * np + 1], ql, b2, b3);
+                    mma16<F16>(s[2 * np], qh, c0, c1);
+                    mma16<F16>(s[2 * np + 1], qh, c2, c3);
+                    mma16<F16>(s[2 * np], qh, b0, b1);
+                    mma16<F16>(s[2 * np + 1], qh, b2, b3);
+                } else {
+                    mma16<F16>(s[2 * np], qf[ks], b0, b1);
+                    mma16<F16>(s[2 * np + 1], qf[ks], b2, b3);
+                }
             }
         }
         // scale (in log2 units), mask, online softmax
@@ -216,7 +254,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
             m_new[r] = fmaxf(m_i[r], mx[r]);
             alpha[r] = m_new[r] == -INFINITY ? 1.0f : exp2f(m_i[r] - m_new[r]);
         }
-        uint32_t pf[4][4];  // P as bf16 A fragments: 4 key steps of 16
+        uint32_t pf[4][4];  // P as 16-bit A fragments: 4 key steps of 16
+        uint32_t pl[SPLIT ? 4 : 1][4];  // SPLIT: lo parts of P
 #pragma unroll
         for (int n = 0; n < 8; n++) {
             float p[4];
@@ -229,6 +268,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
             // C-fragment (rows r, r+8; cols 2c, 2c+1) -> A-fragment halves of key step n/2
             pf[n >> 1][(n & 1) * 2 + 0] = pack16<F16>(p[0], p[1]);
             pf[n >> 1][(n & 1) * 2 + 1] = pack16<F16>(p[2], p[3]);
+            if (SPLIT) {
+                float l[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    l[e] = __fsub_rn(p[e], __half2float(__float2half_rn(p[e])));
+                }
+                pl[SPLIT ? (n >> 1) : 0][(n & 1) * 2 + 0] = pack16<F16>(l[0], l[1]);
+                pl[SPLIT ? (n >> 1) : 0][(n & 1) * 2 + 1] = pack16<F16>(l[2], l[3]);
+            }
         }
 #pragma unroll
         for (int r = 0; r < 2; r++) {
@@ -255,6 +303,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
                 const int key = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
                 const int d   = np * 16 + (lane >> 4) * 8;
                 ldsm_x4_t(b0, b1, b2, b3, Vb + key * kAttnPad + d);
+                if (SPLIT) {
+                    uint32_t c0, c1, c2, c3;
+                    ldsm_x4_t(c0, c1, c2, c3, Vbl + key * kAttnPad + d);
+                    const uint32_t lf[4] = { pl[SPLIT ? ks : 0][0], pl[SPLIT ? ks : 0][1], pl[SPLIT ? ks : 0][2],
+                                             pl[SPLIT ? ks : 0][3] };
+                    mma16<F16>(o[2 * np], lf, b0, b1);
+                    mma16<F16>(o[2 * np + 1], lf, b2, b3);
+                    mma16<F16>(o[2 * np], af, c0, c1);
+                    mma16<F16>(o[2 * np + 1], af, c2, c3);
+                }
                 mma16<F16>(o[2 * np], af, b0, b1);
                 mma16<F16>(o[2 * np + 1], af, b2, b3);
             }
@@ -295,11 +353,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
 
 using namespace acb;
 
-extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs,
-                                       int64_t k_ts, const void * v, int64_t v_bs, int64_t v_ts, void * o,
-                                       int o_type, int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
-                                       int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
-                                       int flags, acb_stream_t stream) {
+static acb_status attn_launch(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs, int64_t k_ts,
+                              const void * v, int64_t v_bs, int64_t v_ts, void * o, int o_type, int64_t o_bs,
+                              int64_t o_ts, int batch, int Sq, int Skv, int Nh, int Nkv, int head_dim, int mask,
+                              int window, int causal_off, float scale, int flags, bool split, int64_t q_lo,
+                              int64_t k_lo, int64_t v_lo, acb_stream_t stream) {
     if (!q || !k || !v || !o || batch <= 0 || Sq <= 0 || Skv <= 0 || Nh <= 0 || Nkv <= 0 || Nh % Nkv != 0) {
         return ACB_ERR_INVALID_ARG;
     }
@@ -307,8 +365,9 @@ extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_t
         mask < 0 || mask > 2) {
         return ACB_ERR_UNSUPPORTED;
     }
-    if ((q_ts | k_ts | v_ts | q_bs | k_bs | v_bs) % 8 != 0 || reinterpret_cast<uintptr_t>(q) % 16 ||
-        reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16) {
+    if ((q_ts | k_ts | v_ts | q_bs | k_bs | v_bs | q_lo | k_lo | v_lo) % 8 != 0 ||
+        reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(k) % 16 ||
+        reinterpret_cast<uintptr_t>(v) % 16) {
         return ACB_ERR_UNSUPPORTED;  // 16-byte cp.async rows
     }
     AttnArgs a   = {};
@@ -333,7 +392,10 @@ extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_t
     a.window     = window;
     a.causal_off = causal_off;
     a.scale_log2 = scale * 1.4426950408889634f;
-    const size_t smem = (size_t) (kAttnBQ + 4 * kAttnBK) * kAttnPad * 2;
+    a.q_lo       = q_lo;
+    a.k_lo       = k_lo;
+    a.v_lo       = v_lo;
+    const size_t smem = (size_t) (split ? 10 : 5) * kAttnBQ * kAttnPad * 2;
     const dim3   grid((unsigned) ((Sq + kAttnBQ - 1) / kAttnBQ), (unsigned) Nh, (unsigned) batch);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim            = grid;
@@ -343,13 +405,21 @@ extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_t
     cudaLaunchAttribute attr[1];
     attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs                                          = (flags & 1) ? attr : nullptr;
-    cfg.numAttrs                                       = (flags & 1) ? 1 : 0;
-    const bool f16 = (flags & ACB_FLAG_F16) != 0;
-    void (*kern)(const AttnArgs) =
-        mask == MASK_CAUSAL ? (f16 ? attn_prefill_kernel<MASK_CAUSAL, true> : attn_prefill_kernel<MASK_CAUSAL, false>)
-        : mask == MASK_WINDOW ? (f16 ? attn_prefill_kernel<MASK_WINDOW, true> : attn_prefill_kernel<MASK_WINDOW, false>)
-                              : (f16 ? attn_prefill_kernel<MASK_NONE, true> : attn_prefill_kernel<MASK_NONE, false>);
+    cfg.attrs                                          = (flags & ACB_FLAG_PDL) ? attr : nullptr;
+    cfg.numAttrs                                       = (flags & ACB_FLAG_PDL) ? 1 : 0;
+    const bool f16 = split || (flags & ACB_FLAG_F16) != 0;
+    void (*kern)(const AttnArgs) = nullptr;
+#define ACB_PICK(M)                                                                                      \
+    kern = split ? attn_prefill_kernel<M, true, true>                                                    \
+                 : (f16 ? attn_prefill_kernel<M, true, false> : attn_prefill_kernel<M, false, false>)
+    if (mask == MASK_CAUSAL) {
+        ACB_PICK(MASK_CAUSAL);
+    } else if (mask == MASK_WINDOW) {
+        ACB_PICK(MASK_WINDOW);
+    } else {
+        ACB_PICK(MASK_NONE);
+    }
+#undef ACB_PICK
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     if (e != cudaSuccess) {
@@ -357,4 +427,26 @@ extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_t
         return ACB_ERR_CUDA;
     }
     return ACB_OK;
+}
+
+extern "C" acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs,
+                                       int64_t k_ts, const void * v, int64_t v_bs, int64_t v_ts, void * o,
+                                       int o_type, int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
+                                       int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
+                                       int flags, acb_stream_t stream) {
+    return attn_launch(q, q_bs, q_ts, k, k_bs, k_ts, v, v_bs, v_ts, o, o_type, o_bs, o_ts, batch, Sq, Skv, Nh, Nkv,
+                       head_dim, mask, window, causal_off, scale, flags, false, 0, 0, 0, stream);
+}
+
+extern "C" acb_status acb_attn_prefill_split(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs,
+                                             int64_t k_ts, const void * v, int64_t v_bs, int64_t v_ts, void * o,
+                                             int o_type, int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv,
+                                             int Nh, int Nkv, int head_dim, int mask, int window, int causal_off,
+                                             float scale, int flags, int64_t q_lo, int64_t k_lo, int64_t v_lo,
+                                             acb_stream_t stream) {
+    if (q_lo == 0 || k_lo == 0 || v_lo == 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    return attn_launch(q, q_bs, q_ts, k, k_bs, k_ts, v, v_bs, v_ts, o, o_type, o_bs, o_ts, batch, Sq, Skv, Nh, Nkv,
+                       head_dim, mask, window, causal_off, scale, flags, true, q_lo, k_lo, v_lo, stream);
 }

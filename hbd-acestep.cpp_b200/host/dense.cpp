@@ -1,0 +1,74 @@
+// dense.cpp -- tensor-core linears with the reference's quantised mul_mat arithmetic.
+#include "dense.h"
+
+#include "host_common.h"
+
+namespace acb {
+
+static bool splits_weights(int vec) {
+    return vec == ACB_TYPE_Q8_0 || vec == ACB_TYPE_Q8_K;
+}
+
+size_t DenseLinear::elems(const std::vector<DevTensor *> & parts) {
+    size_t n = 0;
+    for (const DevTensor * t : parts) {
+        n += (size_t) t->N * (size_t) t->K;
+    }
+    return parts.empty() ? 0 : n * (splits_weights(acb_vec_dot_type(parts[0]->type)) ? 3 : 1);
+}
+
+acb_status dense_build(DenseLinear & L, const std::vector<DevTensor *> & parts, uint16_t * dst, const int32_t * ids,
+                       float * tmp, cudaStream_t st) {
+    if (parts.empty()) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int vt = acb_vec_dot_type(parts[0]->type);
+    if (vt < 0) {
+        set_last_error("weight type without a tensor-core path");
+        return ACB_ERR_UNSUPPORTED;
+    }
+    for (const DevTensor * t : parts) {
+        if (acb_vec_dot_type(t->type) != vt || t->K != parts[0]->K) {
+            set_last_error("stacked projections with different vec-dot types or widths");
+            return ACB_ERR_UNSUPPORTED;
+        }
+    }
+    const int64_t K = parts[0]->K;
+    L.w             = dst;
+    L.vec           = vt;
+    L.op            = vt == ACB_TYPE_BF16 ? 0 : ACB_FLAG_F16;
+    L.K             = (int) K;
+    L.split         = splits_weights(vt);
+    L.ldw           = L.split ? 3 * K : K;
+    int64_t rows    = 0;
+    for (const DevTensor * t : parts) {
+        uint16_t * d = dst + rows * L.ldw;
+        if (L.split) {
+            // exact f32 dequantisation, then the [hi | lo | hi] split of every value
+            ACB_TRY(acb_get_rows(t->data, t->type, t->N, K, ids, t->N, tmp, ACB_TYPE_F32, K, nullptr,
+                                 (acb_stream_t) st));
+            ACB_TRY(acb_act_quant_ex(tmp, K, 0, t->N, K, ACB_TYPE_F16, ACB_LAYOUT_GEMM_B, d, ACB_TYPE_F16, L.ldw, 0,
+                                     (acb_stream_t) st));
+        } else {
+            ACB_TRY(acb_get_rows(t->data, t->type, t->N, K, ids, t->N, d, L.act_type(), K, nullptr,
+                                 (acb_stream_t) st));
+        }
+        rows += t->N;
+    }
+    L.N = (int) rows;
+    return ACB_OK;
+}
+
+acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int64_t xs, int64_t up_off, int M,
+                         void * C, int c_type, int64_t ldc, const float * bias, const float * res, int64_t ldr,
+                         const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
+                         cudaStream_t st) {
+    const bool    three  = exact && L.split;
+    const int64_t Kp     = three ? 3 * (int64_t) L.K : L.K;
+    const int     layout = three ? ACB_LAYOUT_GEMM_A : ACB_LAYOUT_PLAIN;
+    ACB_TRY(acb_act_quant_ex(x, xs, up_off, M, L.K, L.vec, layout, s.xq, L.act_type(), Kp, 0, (acb_stream_t) st));
+    return acb_gemm_tc(s.xq, Kp, L.w, L.ldw, M, L.N, Kp, C, c_type, ldc, bias, res, ldr, gate, gate_stride,
+                       rows_per_sample, ACB_FLAG_PDL | L.op, s.ws, s.ws_bytes, s.err, (acb_stream_t) st);
+}
+
+}  // namespace acb

@@ -1,0 +1,61 @@
+// dense.h -- the tensor-core linear shared by the prefill-shaped drivers (text encoder, DiT):
+// ggml_mul_mat(W, x) at M = tokens (src/qwen3-enc.h:86-88, src/dit-graph.h:36-49) over a
+// resident 16-bit copy of W, with the activation quantised the way ggml's quantised mul_mat
+// does it (acb_act_quant_ex).
+//
+// Two arithmetic modes share one weight copy:
+//   exact  quantised weights are stored as [hi | lo | hi] f16 along K (hi + lo == the dequantised
+//          value) and the activation as [hi | hi | lo]; one GEMM over 3K then forms every
+//          product of the reference's dequantised operands to ~2^-22 and accumulates in fp32,
+//          so results track the reference CPU build to fp32 summation order;
+//   fast   the GEMM reads only the hi columns (K): f16 operands, 3x less tensor work, f16
+//          rounding of both operands.
+// F16 and BF16 weights are exact in one pass (ggml rounds the activation to the weight type).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <vector>
+
+#include "../../include/acb.h"
+#include "weights.h"
+
+namespace acb {
+
+struct DenseLinear {
+    uint16_t * w     = nullptr;  // [N][ldw] 16-bit
+    int64_t    ldw   = 0;        // K, or 3K when split
+    int        N     = 0;
+    int        K     = 0;
+    int        vec   = -1;     // ggml vec-dot type of the source weights
+    int        op    = 0;      // ACB_FLAG_F16 or 0 (bf16 operands)
+    bool       split = false;  // weights stored as [hi | lo | hi]
+
+    int act_type() const { return op ? ACB_TYPE_F16 : ACB_TYPE_BF16; }
+
+    // 16-bit elements of the stored copy of `parts` stacked by rows
+    static size_t elems(const std::vector<DevTensor *> & parts);
+};
+
+// Build the resident copy of `parts` stacked by row concatenation (gf_load_qkv_fused /
+// gf_load_pair_fused, src/gguf-weights.h:281-354) at dst. ids: device int32 0..max rows-1;
+// tmp: device f32 scratch of max N*K floats. Enqueued on st.
+acb_status dense_build(DenseLinear & L, const std::vector<DevTensor *> & parts, uint16_t * dst, const int32_t * ids,
+                       float * tmp, cudaStream_t st);
+
+// Scratch of one dense call: the quantised activation and the split-K workspace.
+struct DenseScratch {
+    void *  xq       = nullptr;  // >= rows * 3K 16-bit elements
+    void *  ws       = nullptr;
+    size_t  ws_bytes = 0;
+    int *   err      = nullptr;
+};
+
+// C[M][N] = epi(x . W^T): x f32 [M][xs] (with up_off > 0: silu(x) * x[up_off + .], the SwiGLU
+// input of a down projection); bias f32 [N] optional; res/gate as acb_gemm_tc.
+acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int64_t xs, int64_t up_off, int M,
+                         void * C, int c_type, int64_t ldc, const float * bias, const float * res, int64_t ldr,
+                         const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
+                         cudaStream_t st);
+
+}  // namespace acb

@@ -1,24 +1,22 @@
 // qwen3_enc.cpp -- the Qwen3 encoder stack of acestep.cpp (src/qwen3-enc.h) on libacb kernels.
 //
-// Prefill over a whole prompt is GEMM-shaped, so every linear runs on the tcgen05 tensor-core
-// GEMM over resident f16 copies of the weights (dequantised exactly from their GGUF blocks at
-// load, then rounded to f16), with the activation quantised the way ggml's quantised mul_mat
-// does it (acb_act_quant), so the products are the reference's up to f16 rounding. One forward
-// for S tokens, per layer:
+// Prefill over a whole prompt is GEMM-shaped, so every linear is a tensor-core GEMM (dense.h)
+// over a resident 16-bit copy of the weights with the activation quantised like ggml's
+// quantised mul_mat. In the default exact mode products are formed from hi/lo f16 splits of the
+// reference's own dequantised operands and attention likewise (acb_attn_prefill_split), so the
+// result tracks the reference CPU build to fp32 summation order; fast mode uses single f16
+// operands. One forward for S tokens, per layer:
 //   RMSNorm * input_layernorm                h (f32)       -> xn (f32)
-//   activation quantisation                  xn            -> xq (f16)
-//   GEMM  Q||K||V                            xq            -> qkv (f16 [S][(Nh+2Nkv)D])
-//   q/k RMSNorm + NeoX RoPE (2 launches)     qkv columns   -> q, k (f16, head-contiguous)
-//   flash attention, causal                  q, k, v = qkv column view -> att (f32)
-//   activation quantisation                  att           -> xq
-//   GEMM  o_proj, epilogue + h               xq            -> h (in place)
+//   quantise + GEMM  Q||K||V                 xn            -> qkv (f32 exact / f16 fast)
+//   q/k RMSNorm + NeoX RoPE (2 launches)     qkv columns   -> in place (exact) / q, k (fast)
+//   hi/lo planes of Q||K||V (exact)          qkv           -> planes
+//   flash attention, causal                  q, k, v views -> att (f32)
+//   quantise + GEMM  o_proj, epilogue + h    att           -> h (in place)
 //   RMSNorm * post_attention_layernorm       h             -> xn
-//   activation quantisation                  xn            -> xq
-//   GEMM  gate||up                           xq            -> gu (f32 [S][2F])
-//   SwiGLU + activation quantisation         gu            -> xq [S][F]
-//   GEMM  down_proj, epilogue + h            xq            -> h (in place)
-// then the final RMSNorm into f32 output. The chain for each S is captured once as a CUDA
-// graph (tensor-core launches with programmatic dependent launch) and replayed.
+//   quantise + GEMM  gate||up                xn            -> gu (f32 [S][2F])
+//   SwiGLU + quantise + GEMM down, + h       gu            -> h (in place)
+// then the final RMSNorm into f32 output. The chain for each (S, mode) is captured once as a
+// CUDA graph (tensor-core launches with programmatic dependent launch) and replayed.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -29,6 +27,7 @@
 #include <vector>
 
 #include "../../include/acb_models.h"
+#include "dense.h"
 #include "gguf.h"
 #include "host_common.h"
 #include "weights.h"
@@ -37,20 +36,9 @@ using namespace acb;
 
 namespace {
 
-// One tensor-core linear: resident 16-bit weight rows, the activation format it expects and the
-// GEMM operand flag.
-struct Lin {
-    uint16_t * w   = nullptr;  // [N][K] f16 (bf16 for BF16 weights)
-    int        vec = -1;       // ggml vec-dot type of the source weights
-    int        op  = 0;        // ACB_FLAG_F16 or 0 (bf16 operands)
-    int        N = 0, K = 0;
-
-    int act_type() const { return op ? ACB_TYPE_F16 : ACB_TYPE_BF16; }
-};
-
 struct EncLayer {
-    DevTensor *attn_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
-    Lin        qkv, o, gu, down;
+    DevTensor * attn_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    DenseLinear qkv, o, gu, down;
 };
 
 constexpr int kPdl = ACB_FLAG_PDL;
@@ -64,12 +52,13 @@ struct acb_qwen3_enc {
     DevBuf                w16;    // every linear, 16-bit
     DevTensor *           embed = nullptr, *final_norm = nullptr;
     std::vector<EncLayer> layers;
-    cudaStream_t          st = nullptr;
+    cudaStream_t          st    = nullptr;
+    bool                  exact = true;
 
     // scratch for up to cap tokens
     int                            cap = 0;
-    DevBuf                         ids, pos, rope, h, xn, xq, qkv, q, k, att, gu, out, err, ws;
-    std::map<int, cudaGraphExec_t> graphs;  // one per S
+    DevBuf                         ids, pos, rope, h, xn, xq, qkv, qkv32, planes, q, k, att, gu, out, err, ws;
+    std::map<int, cudaGraphExec_t> graphs;  // one per S * 2 + exact
 
     ~acb_qwen3_enc() {
         cudaSetDevice(device);
@@ -89,8 +78,7 @@ struct acb_qwen3_enc {
     int nqkv() const { return (c.n_heads + 2 * c.n_kv_heads) * c.head_dim; }
 
     acb_status reserve(int S);
-    acb_status linear(const Lin & L, const float * x, int64_t xs, int S, void * C, int c_type, int64_t ldc,
-                      const float * res, cudaStream_t s);
+    DenseScratch scratch() { return DenseScratch{ xq.p, ws.p, ws.bytes, err.as<int>() }; }
     acb_status enqueue_layers(int S, int l0, int l1, cudaStream_t s);
     acb_status enqueue(int S, cudaStream_t s);
     acb_status run(int S, cudaStream_t s);
@@ -110,8 +98,10 @@ acb_status acb_qwen3_enc::reserve(int S) {
     bad |= pos.alloc((size_t) n * 4, false) != ACB_OK;
     bad |= h.alloc((size_t) n * H * 4) != ACB_OK;
     bad |= xn.alloc((size_t) n * H * 4) != ACB_OK;
-    bad |= xq.alloc((size_t) n * XQ * 2) != ACB_OK;
+    bad |= xq.alloc((size_t) n * XQ * 3 * 2) != ACB_OK;
     bad |= qkv.alloc((size_t) n * nqkv() * 2) != ACB_OK;
+    bad |= qkv32.alloc((size_t) n * nqkv() * 4) != ACB_OK;
+    bad |= planes.alloc((size_t) n * nqkv() * 2 * 2) != ACB_OK;
     bad |= q.alloc((size_t) n * QD * 2) != ACB_OK;
     bad |= k.alloc((size_t) n * KD * 2) != ACB_OK;
     bad |= att.alloc((size_t) n * QD * 4) != ACB_OK;
@@ -123,8 +113,11 @@ acb_status acb_qwen3_enc::reserve(int S) {
         size_t wsb = 0;
         for (int m = 128; m < n + 128; m += 128) {
             const int64_t M = std::min(m, n);
-            wsb = std::max({ wsb, acb_gemm_workspace_bytes(M, nqkv(), H), acb_gemm_workspace_bytes(M, H, QD),
-                             acb_gemm_workspace_bytes(M, 2 * F, H), acb_gemm_workspace_bytes(M, H, F) });
+            for (int64_t km : { (int64_t) 1, (int64_t) 3 }) {
+                wsb = std::max({ wsb, acb_gemm_workspace_bytes(M, nqkv(), km * H),
+                                 acb_gemm_workspace_bytes(M, H, km * QD), acb_gemm_workspace_bytes(M, 2 * F, km * H),
+                                 acb_gemm_workspace_bytes(M, H, km * F) });
+            }
         }
         bad |= ws.alloc(wsb, false) != ACB_OK;
     }
@@ -150,45 +143,63 @@ acb_status acb_qwen3_enc::reserve(int S) {
     return ACB_OK;
 }
 
-// ggml_mul_mat(W, x) for S rows of f32 activations: quantise x like ggml, then the GEMM (with
-// the residual add fused when res is given).
-acb_status acb_qwen3_enc::linear(const Lin & L, const float * x, int64_t xs, int S, void * C, int c_type,
-                                 int64_t ldc, const float * res, cudaStream_t s) {
-    ACB_TRY(acb_act_quant(x, xs, S, L.K, L.vec, xq.p, L.act_type(), L.K, (acb_stream_t) s));
-    return acb_gemm_tc(xq.p, L.K, L.w, L.K, S, L.N, L.K, C, c_type, ldc, nullptr, res, res ? ldc : 0, nullptr, 0, 0,
-                       kPdl | L.op, ws.p, ws.bytes, err.as<int>(), (acb_stream_t) s);
-}
-
 // Layers [l0, l1) over the hidden states in `h` (qwen3_build_layers, qwen3-enc.h:249-262).
 acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) {
-    const int    H = c.hidden_size, F = c.intermediate_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
-    const int    QD = Nh * D, KD = Nkv * D, NQKV = nqkv();
-    const float  eps   = c.rms_norm_eps;
-    const float  scale = 1.0f / sqrtf((float) D);
-    acb_stream_t as    = (acb_stream_t) s;
-    int *        e     = err.as<int>();
-    float *      hp    = h.as<float>();
-    float *      xp    = xn.as<float>();
+    const int          H = c.hidden_size, F = c.intermediate_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
+    const int          QD = Nh * D, KD = Nkv * D, NQKV = nqkv();
+    const float        eps   = c.rms_norm_eps;
+    const float        scale = 1.0f / sqrtf((float) D);
+    const acb_stream_t as    = (acb_stream_t) s;
+    const DenseScratch sc    = scratch();
+    int *              e     = err.as<int>();
+    float *            hp    = h.as<float>();
+    float *            xp    = xn.as<float>();
+    const int          mask  = c.is_causal ? 1 : 0;
     for (int l = l0; l < l1; l++) {
         const EncLayer & L = layers[(size_t) l];
         ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.attn_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
                              as));
-        ACB_TRY(linear(L.qkv, xp, H, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, s));
-        ACB_TRY(acb_qk_norm_rope(qkv.p, ACB_TYPE_F16, NQKV, q.p, ACB_TYPE_F16, QD, D, 0, S, Nh, D,
-                                 (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e, as));
-        ACB_TRY(acb_qk_norm_rope(qkv.as<uint16_t>() + QD, ACB_TYPE_F16, NQKV, k.p, ACB_TYPE_F16, KD, D, 0, S, Nkv, D,
-                                 (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
-                                 as));
-        ACB_TRY(acb_attn_prefill(q.p, (int64_t) S * QD, QD, k.p, (int64_t) S * KD, KD, qkv.as<uint16_t>() + QD + KD,
-                                 (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, 1, S, S, Nh, Nkv,
-                                 D, c.is_causal ? 1 : 0, 0, 0, scale, kPdl | ACB_FLAG_F16, as));
-        ACB_TRY(linear(L.o, att.as<float>(), QD, S, hp, ACB_TYPE_F32, H, hp, s));
+        if (exact) {
+            float * q32 = qkv32.as<float>();
+            ACB_TRY(dense_forward(L.qkv, true, xp, H, 0, S, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0,
+                                  0, sc, s));
+            // q/k norm + rope in place (each warp reads its whole head before writing it)
+            ACB_TRY(acb_qk_norm_rope(q32, ACB_TYPE_F32, NQKV, q32, ACB_TYPE_F32, NQKV, D, 0, S, Nh, D,
+                                     (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
+                                     as));
+            ACB_TRY(acb_qk_norm_rope(q32 + QD, ACB_TYPE_F32, NQKV, q32 + QD, ACB_TYPE_F32, NQKV, D, 0, S, Nkv, D,
+                                     (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
+                                     as));
+            const int64_t lo = (int64_t) cap * NQKV;
+            uint16_t *    hi = planes.as<uint16_t>();
+            ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, S, NQKV, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, NQKV, lo,
+                                     as));
+            ACB_TRY(acb_attn_prefill_split(hi, (int64_t) S * NQKV, NQKV, hi + QD, (int64_t) S * NQKV, NQKV,
+                                           hi + QD + KD, (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32,
+                                           (int64_t) S * QD, QD, 1, S, S, Nh, Nkv, D, mask, 0, 0, scale, kPdl, lo, lo,
+                                           lo, as));
+        } else {
+            ACB_TRY(dense_forward(L.qkv, false, xp, H, 0, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
+                                  0, sc, s));
+            ACB_TRY(acb_qk_norm_rope(qkv.p, ACB_TYPE_F16, NQKV, q.p, ACB_TYPE_F16, QD, D, 0, S, Nh, D,
+                                     (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
+                                     as));
+            ACB_TRY(acb_qk_norm_rope(qkv.as<uint16_t>() + QD, ACB_TYPE_F16, NQKV, k.p, ACB_TYPE_F16, KD, D, 0, S, Nkv,
+                                     D, (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap,
+                                     e, as));
+            ACB_TRY(acb_attn_prefill(q.p, (int64_t) S * QD, QD, k.p, (int64_t) S * KD, KD,
+                                     qkv.as<uint16_t>() + QD + KD, (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32,
+                                     (int64_t) S * QD, QD, 1, S, S, Nh, Nkv, D, mask, 0, 0, scale, kPdl | ACB_FLAG_F16,
+                                     as));
+        }
+        ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
+                              0, sc, s));
         ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.post_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
                              as));
-        ACB_TRY(linear(L.gu, xp, H, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, s));
-        ACB_TRY(acb_act_quant_swiglu(gu.as<float>(), 2 * F, F, S, F, L.down.vec, xq.p, L.down.act_type(), F, as));
-        ACB_TRY(acb_gemm_tc(xq.p, F, L.down.w, F, S, H, F, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
-                            kPdl | L.down.op, ws.p, ws.bytes, e, as));
+        ACB_TRY(dense_forward(L.gu, exact, xp, H, 0, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0,
+                              sc, s));
+        ACB_TRY(dense_forward(L.down, exact, gu.as<float>(), 2 * F, F, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr,
+                              0, 0, sc, s));
     }
     return ACB_OK;
 }
@@ -206,7 +217,8 @@ acb_status acb_qwen3_enc::enqueue(int S, cudaStream_t s) {
 
 // Replay (capturing on first use) the graph for S on stream s.
 acb_status acb_qwen3_enc::run(int S, cudaStream_t s) {
-    auto it = graphs.find(S);
+    const int key = S * 2 + (exact ? 1 : 0);
+    auto      it  = graphs.find(key);
     if (it == graphs.end()) {
         cudaGraph_t g = nullptr;
         if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
@@ -228,7 +240,7 @@ acb_status acb_qwen3_enc::run(int S, cudaStream_t s) {
             set_last_error("encoder graph instantiation failed");
             return ACB_ERR_CUDA;
         }
-        it = graphs.emplace(S, ex).first;
+        it = graphs.emplace(key, ex).first;
     }
     return cudaGraphLaunch(it->second, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
 }
@@ -330,19 +342,22 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
     ACB_TRY(A.upload(m->st));
     ACB_TRY(stage->upload(m->st));
 
-    // 16-bit copies, every matrix on a 256-byte boundary
-    const size_t per_layer[4] = { (size_t) (QD + 2 * KD) * H, (size_t) H * QD, (size_t) 2 * F * H, (size_t) H * F };
-    size_t       layer_bytes  = 0;
-    for (size_t n : per_layer) {
-        layer_bytes += (n * 2 + 255) & ~size_t(255);
+    // 16-bit copies ([hi | lo | hi] for quantised weights), every matrix on a 256-byte boundary
+    size_t total = 0;
+    for (const Raw & R : raw) {
+        for (const std::vector<DevTensor *> & parts : { R.qkv, std::vector<DevTensor *>{ R.o }, R.gu,
+                                                         std::vector<DevTensor *>{ R.down } }) {
+            total += (DenseLinear::elems(parts) * 2 + 255) & ~size_t(255);
+        }
     }
-    if (m->w16.alloc(layer_bytes * (size_t) c.n_layers, false) != ACB_OK) {
+    if (m->w16.alloc(total, false) != ACB_OK) {
         return bad(ACB_ERR_OOM, "16-bit weight allocation failed");
     }
-    DevBuf        idbuf;
+    DevBuf        idbuf, tmp;
     const int64_t max_rows = std::max<int64_t>({ (int64_t) QD, (int64_t) F, (int64_t) H });
-    if (idbuf.alloc((size_t) max_rows * 4, false) != ACB_OK) {
-        return bad(ACB_ERR_OOM, "id buffer allocation failed");
+    if (idbuf.alloc((size_t) max_rows * 4, false) != ACB_OK ||
+        tmp.alloc((size_t) max_rows * std::max(H, std::max(F, QD)) * 4, false) != ACB_OK) {
+        return bad(ACB_ERR_OOM, "conversion scratch allocation failed");
     }
     {
         std::vector<int32_t> idv((size_t) max_rows);
@@ -353,49 +368,21 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
             return bad(ACB_ERR_CUDA, "id upload failed");
         }
     }
-    // Parts stacked by row concatenation (gf_load_qkv_fused / gf_load_pair_fused,
-    // src/gguf-weights.h:281-354) must share one vec-dot type: the reference only fuses equal
-    // types, and separate matmuls of one activation with different vec-dot types would quantise
-    // it differently.
-    auto build = [&](Lin & L, const std::vector<DevTensor *> & parts, uint16_t * dst) -> acb_status {
-        const int vt = acb_vec_dot_type(parts[0]->type);
-        if (vt < 0) {
-            set_last_error("weight type without a tensor-core path");
-            return ACB_ERR_UNSUPPORTED;
-        }
-        int64_t rows = 0;
-        for (DevTensor * t : parts) {
-            if (acb_vec_dot_type(t->type) != vt) {
-                set_last_error("stacked projections with different vec-dot types");
-                return ACB_ERR_UNSUPPORTED;
-            }
-        }
-        L.w   = dst;
-        L.vec = vt;
-        L.op  = vt == ACB_TYPE_BF16 ? 0 : ACB_FLAG_F16;
-        L.K   = (int) parts[0]->K;
-        for (DevTensor * t : parts) {
-            ACB_TRY(acb_get_rows(t->data, t->type, t->N, t->K, idbuf.as<int32_t>(), t->N, dst + rows * t->K,
-                                 L.act_type(), t->K, nullptr, (acb_stream_t) m->st));
-            rows += t->N;
-        }
-        L.N = (int) rows;
-        return ACB_OK;
-    };
-    uint8_t * base = m->w16.as<uint8_t>();
+    uint8_t * p = m->w16.as<uint8_t>();
     for (int i = 0; i < c.n_layers; i++) {
-        EncLayer & L = m->layers[(size_t) i];
-        Raw &      R = raw[(size_t) i];
-        uint8_t *  p = base + layer_bytes * (size_t) i;
-        uint16_t * w[4];
-        for (int t = 0; t < 4; t++) {
-            w[t] = reinterpret_cast<uint16_t *>(p);
-            p += (per_layer[t] * 2 + 255) & ~size_t(255);
-        }
-        ACB_TRY(build(L.qkv, R.qkv, w[0]));
-        ACB_TRY(build(L.o, { R.o }, w[1]));
-        ACB_TRY(build(L.gu, R.gu, w[2]));
-        ACB_TRY(build(L.down, { R.down }, w[3]));
+        EncLayer & L     = m->layers[(size_t) i];
+        Raw &      R     = raw[(size_t) i];
+        auto       place = [&](DenseLinear & D, const std::vector<DevTensor *> & parts) -> acb_status {
+            ACB_TRY(dense_build(D, parts, reinterpret_cast<uint16_t *>(p), idbuf.as<int32_t>(), tmp.as<float>(),
+                                m->st));
+            p += (DenseLinear::elems(parts) * 2 + 255) & ~size_t(255);
+            // the conversion scratch is reused by the next matrix
+            return cudaStreamSynchronize(m->st) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
+        };
+        ACB_TRY(place(L.qkv, R.qkv));
+        ACB_TRY(place(L.o, { R.o }));
+        ACB_TRY(place(L.gu, R.gu));
+        ACB_TRY(place(L.down, { R.down }));
     }
     if (cudaStreamSynchronize(m->st) != cudaSuccess) {
         return bad(ACB_ERR_CUDA, "weight conversion failed");
@@ -403,6 +390,14 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
     stage.reset();
     ACB_TRY(m->reserve(256));
     *out = m.release();
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_qwen3_set_exact(acb_qwen3_enc * m, int exact) {
+    if (!m) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    m->exact = exact != 0;
     return ACB_OK;
 }
 

@@ -163,6 +163,24 @@ ACB_API acb_status acb_act_quant_swiglu(const float * gu, int64_t gu_stride, int
                                         int64_t F, int vec_type, void * y, int y_type, int64_t y_stride,
                                         acb_stream_t stream);
 
+/* Operand layouts of acb_act_quant_ex. The exact layouts split every value v (each dequantised
+ * operand has at most 18 significant bits: an f16 or f32 scale times a small integer) into
+ * hi = f16(v) and lo = f16(v - hi), which represent it exactly, so that one GEMM over K' = 3K,
+ * A' = [hi|hi|lo] times B' = [hi|lo|hi], sums hi.hi + hi.lo + lo.hi: every product of the
+ * reference's dequantised operands to within 2^-22 relative, accumulated in fp32. */
+enum {
+    ACB_LAYOUT_PLAIN  = 0, /* y[m][k] = operand value */
+    ACB_LAYOUT_GEMM_A = 1, /* y[m][0..3K) = [hi | hi | lo], y_stride >= 3K */
+    ACB_LAYOUT_GEMM_B = 2, /* y[m][0..3K) = [hi | lo | hi] (weights), y_stride >= 3K */
+    ACB_LAYOUT_PLANES = 3, /* hi at y[m][k], lo at y[lo_offset + m*y_stride + k] (attention operands) */
+};
+
+/* acb_act_quant / acb_act_quant_swiglu (up_offset > 0: h = silu(x) * x[up_offset + .]) with an
+ * output layout. */
+ACB_API acb_status acb_act_quant_ex(const float * x, int64_t x_stride, int64_t up_offset, int64_t rows, int64_t K,
+                                    int vec_type, int layout, void * y, int y_type, int64_t y_stride,
+                                    int64_t lo_offset, acb_stream_t stream);
+
 /* Vec-dot type of a weight type (ggml's type_traits_cpu[].vec_dot_type): Q8_0 for Q8_0, Q8_K
  * for Q4_K / Q6_K, the type itself for F16 / BF16; -1 for types without a tensor-core path. */
 ACB_API int acb_vec_dot_type(int weight_type);
@@ -212,6 +230,17 @@ ACB_API acb_status acb_attn_prefill(const void * q, int64_t q_bs, int64_t q_ts, 
                                     int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv, int Nh, int Nkv,
                                     int head_dim, int mask, int window, int causal_off, float scale, int flags,
                                     acb_stream_t stream);
+
+/* acb_attn_prefill with f32-accurate arithmetic: q, k and v point at f16 hi planes whose lo
+ * planes (lo = f16(x - hi), ACB_LAYOUT_PLANES of acb_act_quant_ex) sit q_lo / k_lo / v_lo
+ * elements further; Q.K and P.V are formed as hi.hi + hi.lo + lo.hi on the tensor cores, which
+ * reproduces the reference CPU build's f32 attention (qwen3_attn_f32, src/qwen3-enc.h:101-112;
+ * dit_attn_f32, src/dit-graph.h:123-134) to about 2^-22 relative per product. */
+ACB_API acb_status acb_attn_prefill_split(const void * q, int64_t q_bs, int64_t q_ts, const void * k, int64_t k_bs,
+                                          int64_t k_ts, const void * v, int64_t v_bs, int64_t v_ts, void * o,
+                                          int o_type, int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
+                                          int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
+                                          int flags, int64_t q_lo, int64_t k_lo, int64_t v_lo, acb_stream_t stream);
 
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 

@@ -59,6 +59,10 @@ typedef struct {
  * forms. `device` is the CUDA ordinal the model lives on. */
 ACB_API acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int device, acb_qwen3_enc ** out);
 ACB_API acb_status acb_qwen3_get_config(const acb_qwen3_enc * m, acb_qwen3_config * cfg);
+/* Arithmetic of the linears and attention: exact (the default, nonzero) forms every product of
+ * the reference's dequantised operands from hi/lo f16 splits, tracking the reference CPU build to
+ * fp32 summation order at 3x the tensor work; fast (0) uses single f16 operands. */
+ACB_API acb_status acb_qwen3_set_exact(acb_qwen3_enc * m, int exact);
 ACB_API size_t     acb_qwen3_weight_bytes(const acb_qwen3_enc * m); /* device bytes of all weights */
 
 /* qwen3_forward (qwen3-enc.h:373-448): token ids (host, [S]) -> last-layer hidden states after

@@ -58,3 +58,40 @@ def test_vec_dot_types():
     assert acb.vec_dot_type(acb.Q4_K) == acb.Q8_K and acb.vec_dot_type(acb.Q6_K) == acb.Q8_K
     assert acb.vec_dot_type(acb.F16) == acb.F16 and acb.vec_dot_type(acb.BF16) == acb.BF16
     assert acb.vec_dot_type(acb.F32) == -1
+
+
+def _split(v):
+    hi = v.astype(np.float16)
+    lo = (v - hi.astype(np.float32)).astype(np.float16)
+    return hi, lo
+
+
+@pytest.mark.parametrize("layout", [acb.LAYOUT_GEMM_A, acb.LAYOUT_GEMM_B, acb.LAYOUT_PLANES])
+@pytest.mark.parametrize("vt", [O.Q8_0, O.Q8_K, O.F16])
+def test_act_quant_exact_layouts(cuda, layout, vt):
+    """Exact layouts: hi = f16(v), lo = f16(v - hi) of the same operand values, and hi + lo == v
+    exactly for the dequantised activations (<= 18 significant bits)."""
+    import torch
+    rng = np.random.default_rng(layout * 31 + vt)
+    M, K = 19, 512
+    x = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    y = acb.act_quant_ex(torch.from_numpy(x).to(cuda), K, vt, layout).cpu().numpy()
+    if vt == O.Q8_0:  # the dequantised operand values, unrounded
+        v = O.dequantize(O.quantize(x, O.Q8_0), O.Q8_0, K)
+    elif vt == O.Q8_K:
+        raw = O.quantize(x, O.Q8_K).reshape(M, -1, 292)
+        d = raw[:, :, 0:4].copy().view(np.float32)
+        q = raw[:, :, 4:260].view(np.int8).astype(np.float32)
+        v = (d * q).astype(np.float32).reshape(M, K)
+    else:
+        v = x
+    hi, lo = _split(v)
+    if layout == acb.LAYOUT_GEMM_A:
+        want = np.concatenate([hi, hi, lo], axis=1)
+    elif layout == acb.LAYOUT_GEMM_B:
+        want = np.concatenate([hi, lo, hi], axis=1)
+    else:
+        want = np.concatenate([hi, lo], axis=0)
+    assert_bitexact(y, want, f"layout {layout}")
+    if vt == O.Q8_0:  # f16 scale times a 7-bit integer: the split is exact
+        assert np.array_equal(hi.astype(np.float32) + lo.astype(np.float32), v)

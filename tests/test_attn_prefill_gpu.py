@@ -97,3 +97,35 @@ def test_attn_prefill_f16_operands(cuda, B, Sq, Skv, Nh, Nkv, mask, window):
         assert c >= 0.99999 and r <= 2e-3, (b, c, r)
     oh = acb.attn_prefill(q, k, v, Nh, Nkv, mask=mask, window=window, out_dtype=torch.float16)
     assert max_rel(oh.float().cpu().numpy(), got) <= 2.0 ** -10
+
+
+@pytest.mark.parametrize("B,Sq,Skv,Nh,Nkv,mask,window", [
+    (1, 256, 256, 16, 8, acb.MASK_CAUSAL, 0),
+    (8, 750, 750, 16, 8, acb.MASK_WINDOW, 128),
+    (4, 750, 512, 16, 8, acb.MASK_NONE, 0),
+    (2, 77, 33, 4, 2, acb.MASK_NONE, 0),
+])
+def test_attn_prefill_split_is_fp32_accurate(cuda, B, Sq, Skv, Nh, Nkv, mask, window):
+    """acb_attn_prefill_split on hi/lo planes of f32 Q/K/V: fp32 softmax attention of the f32
+    operands to max_rel <= 2e-6 (the f32 reference CPU attention, qwen3_attn_f32)."""
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(Sq * 5 + Skv + mask)
+    q = torch.randn(B, Sq, Nh * 128, device=cuda, generator=g) * 1.5
+    k = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g) * 1.5
+    v = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g)
+
+    def planes(t):
+        flat = t.reshape(-1, t.shape[-1])
+        pl = acb.act_quant_ex(flat, flat.shape[1], acb.F16, acb.LAYOUT_PLANES)
+        n = flat.shape[0]
+        return pl[:n].view(t.shape), n * flat.shape[1]
+
+    qh, ql = planes(q)
+    kh, kl = planes(k)
+    vh, vl = planes(v)
+    o = acb.attn_prefill_split(qh, kh, vh, ql, kl, vl, Nh, Nkv, mask=mask, window=window)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref = torch_ref(q.double(), k.double(), v.double(), Nh, Nkv, mask, window, 0)
+    got, want = o.double().cpu().numpy(), ref.cpu().numpy()
+    for b in range(B):
+        assert max_rel(got[b], want[b]) <= 2e-6, (b, max_rel(got[b], want[b]))

@@ -6,14 +6,16 @@ dequantised operands on the tensor cores with fp32 accumulation; attention runs 
 Its departures from the reference CPU build are f16 roundings (11-bit significands) and
 summation order.
 
-Bars, per token row, against the oracle in ggml mode:
-  * per layer (the spec's gate: each layer run on the reference's own input hidden states, via
-    acb_qwen3_forward_hidden): cosine >= 0.9999 and max_rel <= 1e-2 for the layer output;
-  * whole stack (ids -> final hidden states): the activation quantisation of every linear turns
-    any tiny difference into whole-quantum flips for values near a rounding boundary, and those
-    compound over layers -- the oracle in exact arithmetic itself sits at row cosine ~0.99991
-    from the ggml oracle after 3 tiny layers -- so the bar is cosine >= 0.9995 and
-    max_rel <= 5e-2, and the GPU must sit closer to the ggml oracle than exact arithmetic does.
+In the default exact mode every product is formed from hi/lo f16 splits of the reference's own
+dequantised operands (and attention likewise), so the pre-quantisation values agree to fp32
+summation order and the activation quantisation flips almost nothing. Bars, per token row,
+against the oracle in ggml mode, per layer (each layer run on the reference's own input hidden
+states, via acb_qwen3_forward_hidden) and for the whole stack: cosine >= 0.9999 and
+max_rel <= 1e-2; and the GPU must sit closer to the ggml oracle than exact arithmetic does (the
+oracle in exact mode departs from ggml by the activation quantisation the GPU reproduces).
+Fast mode (single f16 operands) is checked at full size with looser bars: any f16-level
+difference before a Q8 activation quantiser flips whole quanta for values near a rounding
+boundary, and those compound over the layers.
 The embedding gather is bit-exact.
 """
 import os
@@ -50,7 +52,7 @@ def _check_rows(out, ref, what, cos_bar=0.9999, rel_bar=1e-2):
     return cs, mr
 
 
-def _check_per_layer(enc, om, ids, cfg, cuda):
+def _check_per_layer(enc, om, ids, cfg, cuda, cos_bar=0.9999, rel_bar=1e-2):
     """Run each layer on the oracle's own input to it and compare that layer's output."""
     import torch
     h = om.embed_rows(ids)
@@ -58,7 +60,7 @@ def _check_per_layer(enc, om, ids, cfg, cuda):
     for l in range(cfg["num_hidden_layers"]):
         want = om.run_layers(h, l, l + 1)
         got = enc.forward_hidden(torch.from_numpy(h).to(cuda), l, l + 1).cpu().numpy()
-        cs, mr = _check_rows(got, want, f"layer {l}")
+        cs, mr = _check_rows(got, want, f"layer {l}", cos_bar, rel_bar)
         worst = (min(worst[0], cs), max(worst[1], mr))
         h = want
     return worst
@@ -67,6 +69,7 @@ def _check_per_layer(enc, om, ids, cfg, cuda):
 @pytest.mark.parametrize("policy", ["q8_0", "q4_k_m", "bf16"])
 @pytest.mark.parametrize("S", [77, 256])
 def test_encoder_matches_oracle(cuda, tmp_path, policy, S):
+    """Exact mode (the default): every layer and the whole stack at the spec's bars."""
     pol = {"q8_0": policy_all(O.Q8_0), "q4_k_m": policy_q4_k_m, "bf16": policy_all(O.BF16)}[policy]
     tensors, path = _model(str(tmp_path), ENC_TINY, pol, seed=S)
     enc = acb.Qwen3Encoder(path)
@@ -78,7 +81,7 @@ def test_encoder_matches_oracle(cuda, tmp_path, policy, S):
     om = oracle_model(ENC_TINY, tensors, prefix="")
     ref = om.encode(ids)
     _check_per_layer(enc, om, ids, ENC_TINY, cuda)
-    cs, mr = _check_rows(out, ref, "whole stack vs ggml oracle", 0.9995, 5e-2)
+    cs, mr = _check_rows(out, ref, "whole stack vs ggml oracle")
     if policy != "bf16":
         with O.mul_mat_mode(O.MM_EXACT):
             exact = om.encode(ids)
@@ -150,6 +153,11 @@ def test_encoder_config1_full_depth(cuda, tmp_path):
     tensors = {n: (qt, raw, K, raw.shape[0] if raw.ndim > 1 else 1) for n, (qt, raw, K) in keep.items()}
     om = O.qwen3_from_gguf_tensors(cfg, tensors, prefix="")
     _check_per_layer(enc, om, ids, cfg, cuda)
-    enc.close()
     ref = om.encode(ids)
-    _check_rows(out, ref, "config 1 whole stack vs ggml oracle", 0.9995, 5e-2)
+    _check_rows(out, ref, "config 1 whole stack vs ggml oracle")
+    # fast mode (single f16 operands): the flips of the activation quantisation compound, so its
+    # bars are per layer cosine >= 0.999 / max_rel <= 5e-2 and whole stack cosine >= 0.998
+    enc.set_exact(False)
+    _check_per_layer(enc, om, ids, cfg, cuda, 0.999, 5e-2)
+    _check_rows(enc.forward(ids), ref, "config 1 fast mode whole stack", 0.998, 1e-1)
+    enc.close()

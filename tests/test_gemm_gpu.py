@@ -113,3 +113,22 @@ def test_gemm_split_k(cuda, M, N, K):
     Ch = acb.gemm_bf16(A, B, out_dtype=torch.float16, workspace=ws)
     d = (Ch.float() - base).abs()
     assert (d <= base.abs() * 2.0 ** -10 + 2e-5 * base.abs().max()).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 1024, 3072), (300, 512, 1024)])
+def test_gemm_exact_split_products(cuda, M, N, K):
+    """GEMM over K' = 3K with A' = [hi|hi|lo] and B' = [hi|lo|hi] (acb_act_quant_ex layouts): the
+    product of dequantised Q8_0 activations and weights to fp32 accuracy (max_rel <= 2e-6
+    against float64)."""
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    W = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), O.Q8_0)
+    wd = O.dequantize(W, O.Q8_0, K)
+    xd = O.dequantize(O.quantize(x, O.Q8_0), O.Q8_0, K)
+    A = acb.act_quant_ex(torch.from_numpy(x).to(cuda), K, O.Q8_0, acb.LAYOUT_GEMM_A)
+    B = acb.act_quant_ex(torch.from_numpy(wd).to(cuda), K, O.F16, acb.LAYOUT_GEMM_B)
+    ws = torch.empty(max(1, acb.gemm_workspace_bytes(M, N, 3 * K)), dtype=torch.uint8, device=cuda)
+    C = acb.gemm_bf16(A, B, workspace=ws).double().cpu().numpy()
+    ref = xd.astype(np.float64) @ wd.astype(np.float64).T
+    assert max_rel(C, ref) <= 2e-6, max_rel(C, ref)
