@@ -6,6 +6,7 @@ import numpy as np
 import pytest
 
 import acb
+import oracle as O
 from helpers import max_rel
 
 pytestmark = pytest.mark.gpu
