@@ -100,6 +100,12 @@ def lib():
             "acb_qwen3_embed_lookup": (I, [P, P, I, P]),
             "acb_qwen3_forward_hidden": (I, [P, P, I, I, I, I, P, P]),
             "acb_qwen3_set_exact": (I, [P, I]),
+            "acb_dit_load": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
+            "acb_dit_weight_bytes": (C.c_size_t, [P]),
+            "acb_dit_set_exact": (I, [P, I]),
+            "acb_dit_forward": (I, [P, P, P, I, I, I, F, F, P, I, P]),
+            "acb_dit_generate": (I, [P, P, P, P, I, I, I, I, P, P, F, P]),
+            "acb_dit_free": (None, [P]),
             "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_attn_prefill_split": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I,
                                            I, I, F, I, I64, I64, I64, P]),
@@ -544,4 +550,80 @@ def attn_prefill_split(q, k, v, q_lo, k_lo, v_lo, Nh, Nkv, mask=MASK_NONE, windo
         _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0), v.stride(1),
         _ptr(out), dtype_id(out), out.stride(0), out.stride(1), B, Sq, Skv, Nh, Nkv, 128, mask, window, causal_off,
         scale if scale is not None else 1.0 / math.sqrt(128), flags, q_lo, k_lo, v_lo, _stream(stream)))
+    return out
+
+
+class DiT:
+    """ACE-Step DiT (acb_models.h): dit_ggml_load / one evaluation / dit_ggml_generate."""
+
+    FIELDS = ["n_layers", "hidden_size", "intermediate_size", "n_heads", "n_kv_heads", "head_dim", "in_channels",
+              "out_channels", "patch_size", "sliding_window", "rope_theta", "rms_norm_eps", "enc_hidden_size",
+              "has_null_condition"]
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        import numpy as np
+        self.np = np
+        h = C.c_void_p()
+        st = lib().acb_dit_load(gguf_path.encode(), device, C.byref(h))
+        if st != 0:
+            raise AcbError(f"acb_dit_load ({lib().acb_last_error().decode()})", st)
+        self.h = h
+
+        class Cfg(C.Structure):
+            _fields_ = [(f, C.c_float if f in ("rope_theta", "rms_norm_eps") else C.c_int) for f in DiT.FIELDS]
+        c = Cfg()
+        fn = lib().acb_dit_get_config
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.POINTER(Cfg)]
+        _check("acb_dit_get_config", fn(self.h, C.byref(c)))
+        self.cfg = {f: getattr(c, f) for f in DiT.FIELDS}
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().acb_dit_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def weight_bytes(self) -> int:
+        return lib().acb_dit_weight_bytes(self.h)
+
+    def set_exact(self, exact: bool):
+        _check("acb_dit_set_exact", lib().acb_dit_set_exact(self.h, int(bool(exact))))
+
+    def forward(self, x, enc, t, t_r, n_layers_run=-1, out=None, stream=None):
+        """x [N, T, in_channels], enc [N, enc_S, enc_hidden] f32 CUDA tensors -> velocity [N, T, out_channels]."""
+        import torch
+        N, T, _ = x.shape
+        if out is None:
+            out = torch.empty((N, T, self.cfg["out_channels"]), dtype=torch.float32, device=x.device)
+        _check("acb_dit_forward", lib().acb_dit_forward(self.h, _ptr(x), _ptr(enc), N, T, enc.shape[1], float(t),
+                                                        float(t_r), _ptr(out), n_layers_run, _stream(stream)))
+        return out
+
+    def generate(self, noise, context, enc, schedule, guidance_scale=1.0):
+        """Host arrays: noise [N, T, Oc], context [N, T, in-Oc], enc [N, enc_S, enc_hidden] ->
+        (x0 [N, T, Oc], device ms of the step loop)."""
+        np = self.np
+        noise = np.ascontiguousarray(noise, dtype=np.float32)
+        context = np.ascontiguousarray(context, dtype=np.float32)
+        enc = np.ascontiguousarray(enc, dtype=np.float32)
+        sched = np.ascontiguousarray(schedule, dtype=np.float32)
+        N, T, _ = noise.shape
+        out = np.empty_like(noise)
+        ms = C.c_float(0.0)
+        _check("acb_dit_generate", lib().acb_dit_generate(
+            self.h, noise.ctypes.data, context.ctypes.data, enc.ctypes.data, enc.shape[1], T, N, sched.size,
+            sched.ctypes.data, out.ctypes.data, float(guidance_scale), C.cast(C.pointer(ms), C.c_void_p)))
+        return out, ms.value
+
+
+def turbo_schedule(steps=8, shift=3.0):
+    """t_i = shift*t / (1 + (shift - 1)*t) with t = 1 - i/steps (pipeline-synth-ops.cpp:305-309)."""
+    import numpy as np
+    f = np.float32
+    out = []
+    for i in range(steps):
+        t = f(1.0) - f(i) / f(steps)  # float arithmetic as in the reference
+        out.append(float(f(shift) * t / (f(1.0) + (f(shift) - f(1.0)) * t)))
     return out

@@ -198,6 +198,8 @@ extern "C" int acb_vec_dot_type(int weight_type) {
             return ACB_TYPE_F16;
         case ACB_TYPE_BF16:
             return ACB_TYPE_BF16;
+        case ACB_TYPE_F32:
+            return ACB_TYPE_F32;
         default:
             return -1;
     }
@@ -254,6 +256,10 @@ static acb_status launch_act_quant(const float * x, int64_t x_stride, int64_t up
             break;
         case ACB_TYPE_F16:
             launch_layout<ACB_TYPE_F16, SWIGLU>(layout, grid, st, x, x_stride, up_off, rows, K, y, y_stride, lo_off,
+                                                vin, vout);
+            break;
+        case ACB_TYPE_F32:
+            launch_layout<ACB_TYPE_F32, SWIGLU>(layout, grid, st, x, x_stride, up_off, rows, K, y, y_stride, lo_off,
                                                 vin, vout);
             break;
         case ACB_TYPE_BF16:

@@ -5,8 +5,10 @@
 
 namespace acb {
 
+// Weights whose values are not exact in one 16-bit operand: quantised blocks (f16/f32 scale
+// times an integer) and F32.
 static bool splits_weights(int vec) {
-    return vec == ACB_TYPE_Q8_0 || vec == ACB_TYPE_Q8_K;
+    return vec == ACB_TYPE_Q8_0 || vec == ACB_TYPE_Q8_K || vec == ACB_TYPE_F32;
 }
 
 size_t DenseLinear::elems(const std::vector<DevTensor *> & parts) {

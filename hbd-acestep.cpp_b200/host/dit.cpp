@@ -1,0 +1,831 @@
+// dit.cpp -- the ACE-Step DiT flow-matching denoiser (src/dit.h, src/dit-graph.h,
+// src/dit-sampler.h) on libacb kernels.
+//
+// One evaluation for Ng sequences of S = T / P patches (R = Ng * S rows):
+//   timestep embeddings t and t - t_r -> temb, tproj; modulation vectors for every layer
+//   proj_in (patchify is a reshape of [Ng][T][in_ch]) + bias                 -> h (f32 [R][H])
+//   per layer (dit_ggml_build_layer, dit-graph.h:367-450):
+//     adaLN(h, self_attn_norm, scale_sa, shift_sa) -> Q||K||V -> q/k norm + RoPE -> self
+//       attention (sliding window on even layers) -> o_proj, epilogue h += o * gate_sa
+//     RMSNorm(h, cross_attn_norm) -> q_proj -> q norm -> cross attention over the condition's
+//       K/V (computed once per condition and cached per layer) -> o_proj, epilogue h += o
+//     adaLN(h, mlp_norm, scale_ff, shift_ff) -> gate||up -> SwiGLU -> down, h += o * gate_ff
+//   adaLN(h, norm_out, out_scale, out_shift) -> proj_out + bias -> velocity [Ng][T][out_ch]
+// Linears are tensor-core GEMMs (dense.h; exact mode by default). The generate loop
+// (dit_ggml_generate) runs each denoise step -- embeddings, every layer, CFG/APG, the Euler
+// update -- as one captured CUDA graph; the host only uploads t for the step.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/acb_models.h"
+#include "dense.h"
+#include "gguf.h"
+#include "host_common.h"
+#include "weights.h"
+
+using namespace acb;
+
+namespace {
+
+struct DiTLayerW {
+    DevTensor * sa_norm = nullptr, *sa_q_norm = nullptr, *sa_k_norm = nullptr;
+    DevTensor * ca_norm = nullptr, *ca_q_norm = nullptr, *ca_k_norm = nullptr, *mlp_norm = nullptr;
+    DenseLinear sa_qkv, sa_o, ca_q, ca_kv, ca_o, gu, down;
+};
+
+struct TembW {
+    DenseLinear l1, l2, tp;
+    DevTensor * b1 = nullptr, *b2 = nullptr, *btp = nullptr;
+};
+
+constexpr int kPdl = ACB_FLAG_PDL;
+
+}  // namespace
+
+struct acb_dit {
+    int            device = 0;
+    acb_dit_config c{};
+    cudaStream_t   st    = nullptr;
+    bool           exact = true;
+
+    WeightArena            arena;  // norms, biases, tables (F32), null condition
+    DevBuf                 w16;    // every linear, 16-bit
+    TembW                  te, te_r;
+    DenseLinear            proj_in, cond, proj_out;
+    DevTensor *            proj_in_b = nullptr, *cond_b = nullptr, *norm_out = nullptr, *oss = nullptr;
+    DevTensor *            null_emb = nullptr;
+    DevBuf                 proj_out_b;  // bias [out_ch] repeated over the P patch positions
+    DevBuf                 sst;         // [L][6H]
+    std::vector<DiTLayerW> layers;
+
+    // per-shape scratch
+    int    Ng = 0, S = 0, enc_S = 0;
+    DevBuf tt, sinus, th1, th2, temb2, tproj2, ada, out_ss;
+    DevBuf input, h, xn, xq, qkv32, qkv16, planes, q16, k16, att, gu, vel, pos, rope, ws, err;
+    DevBuf enc_in, enc_h, kv32, kvcache;  // condition: raw [Ng][enc_S][H_enc], embedded, per-layer K/V planes
+    size_t kv_layer_elems = 0;            // elements of one plane of one layer's cached K||V
+    // generate
+    DevBuf                          xt, vt, out, ra;
+    std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
+
+    ~acb_dit() {
+        cudaSetDevice(device);
+        drop_graphs();
+        if (st) {
+            cudaStreamDestroy(st);
+        }
+    }
+
+    void drop_graphs() {
+        for (auto & kv : graphs) {
+            cudaGraphExecDestroy(kv.second);
+        }
+        graphs.clear();
+    }
+
+    int qd() const { return c.n_heads * c.head_dim; }
+    int kvd() const { return c.n_kv_heads * c.head_dim; }
+    int nqkv() const { return qd() + 2 * kvd(); }
+
+    DenseScratch scratch() { return DenseScratch{ xq.p, ws.p, ws.bytes, err.as<int>() }; }
+
+    acb_status reserve(int Ng_, int T, int enc_S_);
+    acb_status timestep(cudaStream_t s);
+    acb_status condition(cudaStream_t s);
+    acb_status evaluate(int n_layers_run, cudaStream_t s);
+    acb_status layer(int l, cudaStream_t s);
+};
+
+// ---- scratch ---------------------------------------------------------------------------------------
+
+acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
+    const int S_ = T / c.patch_size;
+    if (Ng_ == Ng && S_ == S && enc_S_ == enc_S) {
+        return ACB_OK;
+    }
+    drop_graphs();
+    Ng = Ng_, S = S_, enc_S = enc_S_;
+    const size_t R = (size_t) Ng * S, Re = (size_t) Ng * enc_S;
+    const size_t H = c.hidden_size, F = c.intermediate_size, QD = qd(), KD = kvd(), NQKV = nqkv();
+    const size_t in_ch = c.in_channels, P = c.patch_size, Oc = c.out_channels;
+    const size_t XQ = 3 * std::max({ H, F, QD, in_ch * P, (size_t) c.enc_hidden_size, (size_t) 256 });
+    bool         bad = false;
+    auto         A   = [&](DevBuf & b, size_t bytes, bool zero = false) { bad |= b.alloc(bytes, zero) != ACB_OK; };
+    A(tt, 64, true);
+    A(sinus, 2 * 256 * 4);
+    A(th1, 2 * H * 4);
+    A(th2, 2 * H * 4);
+    A(temb2, 2 * H * 4);
+    A(tproj2, 2 * 6 * H * 4);
+    A(ada, (size_t) c.n_layers * 6 * H * 4);
+    A(out_ss, 2 * H * 4);
+    A(input, R * in_ch * P * 4, true);
+    A(h, R * H * 4);
+    A(xn, R * H * 4);
+    A(xq, std::max(R, Re) * XQ * 2);
+    A(qkv32, R * NQKV * 4);
+    A(qkv16, R * NQKV * 2);
+    A(planes, 2 * std::max(R * NQKV, Re * 2 * KD) * 2);
+    A(q16, R * QD * 2);
+    A(k16, R * KD * 2);
+    A(att, R * QD * 4);
+    A(gu, R * 2 * F * 4);
+    A(vel, R * Oc * P * 4);
+    A(enc_in, Re * c.enc_hidden_size * 4);
+    A(enc_h, Re * H * 4);
+    A(kv32, Re * 2 * KD * 4);
+    kv_layer_elems = Re * 2 * KD;
+    A(kvcache, (size_t) c.n_layers * 2 * kv_layer_elems * 2);
+    if (!err.p) {
+        A(err, 4, true);
+    }
+    {
+        // split-K workspace: the largest need over every linear at these row counts (x3 for exact)
+        size_t  wsb = 0;
+        int64_t Ms[3] = { (int64_t) R, (int64_t) Re, 1 };
+        for (int64_t M : Ms) {
+            for (int64_t km : { (int64_t) 1, (int64_t) 3 }) {
+                for (auto nk : { std::make_pair(NQKV, H), std::make_pair(H, QD), std::make_pair(2 * F, H),
+                                 std::make_pair(H, F), std::make_pair(2 * KD, H), std::make_pair(H, in_ch * P),
+                                 std::make_pair(Oc * P, H), std::make_pair(H, (size_t) c.enc_hidden_size),
+                                 std::make_pair(6 * H, H), std::make_pair(H, H), std::make_pair(H, (size_t) 256) }) {
+                    wsb = std::max(wsb, acb_gemm_workspace_bytes(M, (int64_t) nk.first, km * (int64_t) nk.second));
+                }
+            }
+        }
+        A(ws, wsb);
+    }
+    // positions 0..S-1 per sequence and the rope table
+    {
+        std::vector<int32_t> p(R);
+        for (size_t i = 0; i < R; i++) {
+            p[i] = (int32_t) (i % (size_t) S);
+        }
+        std::vector<float> tab((size_t) S * c.head_dim);
+        acb_rope_table_host(tab.data(), S, c.head_dim, c.rope_theta);
+        A(pos, R * 4);
+        A(rope, tab.size() * 4);
+        if (!bad && (cudaMemcpy(pos.p, p.data(), R * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+                     cudaMemcpy(rope.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)) {
+            bad = true;
+        }
+    }
+    if (bad) {
+        Ng = S = enc_S = 0;
+        set_last_error("DiT scratch allocation failed");
+        return ACB_ERR_OOM;
+    }
+    return ACB_OK;
+}
+
+// ---- timestep embedding (dit_ggml_build_temb, dit-graph.h:81-117) -----------------------------------
+
+acb_status acb_dit::timestep(cudaStream_t s) {
+    const int          H  = c.hidden_size;
+    const acb_stream_t as = (acb_stream_t) s;
+    const DenseScratch sc = scratch();
+    ACB_TRY(acb_dit_sinusoid(tt.as<float>(), 256, 10000, sinus.as<float>(), as));
+    for (int r = 0; r < 2; r++) {
+        const TembW & E   = r == 0 ? te : te_r;
+        float *       x0  = sinus.as<float>() + r * 256;
+        float *       a1  = th1.as<float>() + r * H;
+        float *       a2  = th2.as<float>() + r * H;
+        float *       emb = temb2.as<float>() + r * H;
+        ACB_TRY(dense_forward(E.l1, exact, x0, 256, 0, 1, a1, ACB_TYPE_F32, H, (const float *) E.b1->data, nullptr, 0,
+                              nullptr, 0, 0, sc, s));
+        ACB_TRY(acb_silu(a1, a2, H, as));
+        ACB_TRY(dense_forward(E.l2, exact, a2, H, 0, 1, emb, ACB_TYPE_F32, H, (const float *) E.b2->data, nullptr, 0,
+                              nullptr, 0, 0, sc, s));
+        ACB_TRY(acb_silu(emb, a2, H, as));
+        ACB_TRY(dense_forward(E.tp, exact, a2, H, 0, 1, tproj2.as<float>() + r * 6 * H, ACB_TYPE_F32, 6 * H,
+                              (const float *) E.btp->data, nullptr, 0, nullptr, 0, 0, sc, s));
+    }
+    return acb_dit_modulation(sst.as<float>(), tproj2.as<float>(), temb2.as<float>(), (const float *) oss->data,
+                              c.n_layers, H, ada.as<float>(), out_ss.as<float>(), as);
+}
+
+// ---- condition: embedder and every layer's cross-attention K/V (constant across steps) -----------
+
+acb_status acb_dit::condition(cudaStream_t s) {
+    const int          H = c.hidden_size, KD = kvd(), D = c.head_dim;
+    const int          Re = Ng * enc_S;
+    const acb_stream_t as = (acb_stream_t) s;
+    const DenseScratch sc = scratch();
+    ACB_TRY(dense_forward(cond, exact, enc_in.as<float>(), c.enc_hidden_size, 0, Re, enc_h.p, ACB_TYPE_F32, H,
+                          (const float *) cond_b->data, nullptr, 0, nullptr, 0, 0, sc, s));
+    for (int l = 0; l < c.n_layers; l++) {
+        const DiTLayerW & L  = layers[(size_t) l];
+        float *           kv = kv32.as<float>();
+        ACB_TRY(dense_forward(L.ca_kv, exact, enc_h.as<float>(), H, 0, Re, kv, ACB_TYPE_F32, 2 * KD, nullptr, nullptr,
+                              0, nullptr, 0, 0, sc, s));
+        // k RMSNorm (no rope for cross-attention, dit-graph.h:317-331), in place
+        ACB_TRY(acb_qk_norm_rope(kv, ACB_TYPE_F32, 2 * KD, kv, ACB_TYPE_F32, 2 * KD, D, 0, Re, c.n_kv_heads, D,
+                                 (const float *) L.ca_k_norm->data, c.rms_norm_eps, nullptr, nullptr, 0, err.as<int>(),
+                                 as));
+        uint16_t * hi = kvcache.as<uint16_t>() + (size_t) l * 2 * kv_layer_elems;
+        ACB_TRY(acb_act_quant_ex(kv, 2 * KD, 0, Re, 2 * KD, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, 2 * KD,
+                                 (int64_t) kv_layer_elems, as));
+    }
+    return ACB_OK;
+}
+
+// ---- one layer (dit_ggml_build_layer, dit-graph.h:367-450) ----------------------------------------
+
+acb_status acb_dit::layer(int l, cudaStream_t s) {
+    const DiTLayerW &  L = layers[(size_t) l];
+    const int          H = c.hidden_size, D = c.head_dim, Nh = c.n_heads, Nkv = c.n_kv_heads;
+    const int          QD = qd(), KD = kvd(), NQKV = nqkv(), F = c.intermediate_size;
+    const int          R = Ng * S;
+    const float        eps   = c.rms_norm_eps;
+    const float        scale = 1.0f / sqrtf((float) D);
+    const acb_stream_t as    = (acb_stream_t) s;
+    const DenseScratch sc    = scratch();
+    int *              e     = err.as<int>();
+    float *            hp    = h.as<float>();
+    float *            xp    = xn.as<float>();
+    const float *      a     = ada.as<float>() + (size_t) l * 6 * H;
+    const float *shift_sa = a, *scale_sa = a + H, *gate_sa = a + 2 * H;
+    const float *shift_ff = a + 3 * H, *scale_ff = a + 4 * H, *gate_ff = a + 5 * H;
+    // sliding window on even layers when the sequence is longer than the window (dit-sampler.h:253-282)
+    const bool swa  = (l % 2 == 0) && c.sliding_window > 0 && S > c.sliding_window;
+    const int  mask = swa ? 2 : 0;
+
+    // self-attention
+    ACB_TRY(acb_adaln_modulate(hp, ACB_TYPE_F32, (const float *) L.sa_norm->data, eps, scale_sa, shift_sa, 0, xp,
+                               ACB_TYPE_F32, 1, R, H, as));
+    if (exact) {
+        float * q32 = qkv32.as<float>();
+        ACB_TRY(dense_forward(L.sa_qkv, true, xp, H, 0, R, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0, 0,
+                              sc, s));
+        ACB_TRY(acb_qk_norm_rope(q32, ACB_TYPE_F32, NQKV, q32, ACB_TYPE_F32, NQKV, D, 0, R, Nh, D,
+                                 (const float *) L.sa_q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
+                                 as));
+        ACB_TRY(acb_qk_norm_rope(q32 + QD, ACB_TYPE_F32, NQKV, q32 + QD, ACB_TYPE_F32, NQKV, D, 0, R, Nkv, D,
+                                 (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
+                                 as));
+        const int64_t lo = (int64_t) R * NQKV;
+        uint16_t *    hi = planes.as<uint16_t>();
+        ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, R, NQKV, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, NQKV, lo,
+                                 as));
+        ACB_TRY(acb_attn_prefill_split(hi, (int64_t) S * NQKV, NQKV, hi + QD, (int64_t) S * NQKV, NQKV, hi + QD + KD,
+                                       (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng, S, S,
+                                       Nh, Nkv, D, mask, c.sliding_window, 0, scale, kPdl, lo, lo, lo, as));
+    } else {
+        uint16_t * q16p = qkv16.as<uint16_t>();
+        ACB_TRY(dense_forward(L.sa_qkv, false, xp, H, 0, R, q16p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
+                              0, sc, s));
+        ACB_TRY(acb_qk_norm_rope(q16p, ACB_TYPE_F16, NQKV, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
+                                 (const float *) L.sa_q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
+                                 as));
+        ACB_TRY(acb_qk_norm_rope(q16p + QD, ACB_TYPE_F16, NQKV, k16.p, ACB_TYPE_F16, KD, D, 0, R, Nkv, D,
+                                 (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
+                                 as));
+        ACB_TRY(acb_attn_prefill(q16.p, (int64_t) S * QD, QD, k16.p, (int64_t) S * KD, KD, q16p + QD + KD,
+                                 (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng, S, S, Nh,
+                                 Nkv, D, mask, c.sliding_window, 0, scale, kPdl | ACB_FLAG_F16, as));
+    }
+    ACB_TRY(dense_forward(L.sa_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0, R,
+                          sc, s));
+
+    // cross-attention over the cached condition K/V
+    ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.ca_norm->data, xp, ACB_TYPE_F32, H, R, H, eps, as));
+    float * cq = qkv32.as<float>();
+    ACB_TRY(dense_forward(L.ca_q, exact, xp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc, s));
+    ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, cq, ACB_TYPE_F32, QD, D, 0, R, Nh, D,
+                             (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
+    const uint16_t * kv_hi = kvcache.as<uint16_t>() + (size_t) l * 2 * kv_layer_elems;
+    const int64_t    kvlo  = (int64_t) kv_layer_elems;
+    if (exact) {
+        const int64_t lo = (int64_t) R * QD;
+        uint16_t *    qh = planes.as<uint16_t>();
+        ACB_TRY(acb_act_quant_ex(cq, QD, 0, R, QD, ACB_TYPE_F16, ACB_LAYOUT_PLANES, qh, ACB_TYPE_F16, QD, lo, as));
+        ACB_TRY(acb_attn_prefill_split(qh, (int64_t) S * QD, QD, kv_hi, (int64_t) enc_S * 2 * KD, 2 * KD, kv_hi + KD,
+                                       (int64_t) enc_S * 2 * KD, 2 * KD, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng,
+                                       S, enc_S, Nh, Nkv, D, 0, 0, 0, scale, kPdl, lo, kvlo, kvlo, as));
+    } else {
+        ACB_TRY(acb_act_quant(cq, QD, R, QD, ACB_TYPE_F16, q16.p, ACB_TYPE_F16, QD, as));
+        ACB_TRY(acb_attn_prefill(q16.p, (int64_t) S * QD, QD, kv_hi, (int64_t) enc_S * 2 * KD, 2 * KD, kv_hi + KD,
+                                 (int64_t) enc_S * 2 * KD, 2 * KD, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng, S,
+                                 enc_S, Nh, Nkv, D, 0, 0, 0, scale, kPdl | ACB_FLAG_F16, as));
+    }
+    ACB_TRY(dense_forward(L.ca_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
+                          sc, s));
+
+    // FFN
+    ACB_TRY(acb_adaln_modulate(hp, ACB_TYPE_F32, (const float *) L.mlp_norm->data, eps, scale_ff, shift_ff, 0, xp,
+                               ACB_TYPE_F32, 1, R, H, as));
+    ACB_TRY(dense_forward(L.gu, exact, xp, H, 0, R, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0, sc,
+                          s));
+    return dense_forward(L.down, exact, gu.as<float>(), 2 * F, F, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_ff, 0, R,
+                         sc, s);
+}
+
+// ---- one evaluation: input [Ng][T][in_ch] in `input` -> velocity in `vel` ---------------------------
+
+acb_status acb_dit::evaluate(int n_layers_run, cudaStream_t s) {
+    const int          H = c.hidden_size, R = Ng * S, KP = c.in_channels * c.patch_size;
+    const acb_stream_t as = (acb_stream_t) s;
+    const DenseScratch sc = scratch();
+    ACB_TRY(timestep(s));
+    ACB_TRY(dense_forward(proj_in, exact, input.as<float>(), KP, 0, R, h.p, ACB_TYPE_F32, H,
+                          (const float *) proj_in_b->data, nullptr, 0, nullptr, 0, 0, sc, s));
+    const int nl = n_layers_run < 0 || n_layers_run > c.n_layers ? c.n_layers : n_layers_run;
+    for (int l = 0; l < nl; l++) {
+        ACB_TRY(layer(l, s));
+    }
+    const float * o = out_ss.as<float>();
+    ACB_TRY(acb_adaln_modulate(h.p, ACB_TYPE_F32, (const float *) norm_out->data, c.rms_norm_eps, o + H, o, 0, xn.p,
+                               ACB_TYPE_F32, 1, R, H, as));
+    const int NO = c.out_channels * c.patch_size;
+    return dense_forward(proj_out, exact, xn.as<float>(), H, 0, R, vel.p, ACB_TYPE_F32, NO, proj_out_b.as<float>(),
+                         nullptr, 0, nullptr, 0, 0, sc, s);
+}
+
+// ---- loading (dit_ggml_load, src/dit.h:256-420) -----------------------------------------------------
+
+namespace {
+
+// GGUF conv weight [H][ch][P] (ggml ne = [P, ch, H]) to a pre-permuted F32 GEMM weight:
+// proj_in  rows h, element j = p*ch + c  (dit_load_proj_in_w, dit.h:142-195);
+// proj_out rows j = p*ch + c, element h  (dit_load_proj_out_w, dit.h:197-252).
+bool conv_to_f32(const GGUFFile & gf, const std::string & name, int H, int ch, int P, bool out_side,
+                 std::vector<float> & dst) {
+    const GGUFTensor * t = gf.find(name);
+    if (!t || t->ne[0] * t->ne[1] * t->ne[2] * t->ne[3] != (int64_t) H * ch * P) {
+        return false;
+    }
+    auto rd = [&](int64_t i) -> float {
+        const uint8_t * p = static_cast<const uint8_t *>(t->data);
+        uint16_t        v;
+        switch (t->type) {
+            case ACB_TYPE_F32: {
+                float f;
+                memcpy(&f, p + 4 * i, 4);
+                return f;
+            }
+            case ACB_TYPE_F16:
+                memcpy(&v, p + 2 * i, 2);
+                return host_f16_to_f32(v);
+            case ACB_TYPE_BF16:
+                memcpy(&v, p + 2 * i, 2);
+                return host_bf16_to_f32(v);
+            default:
+                return NAN;
+        }
+    };
+    if (t->type != ACB_TYPE_F32 && t->type != ACB_TYPE_F16 && t->type != ACB_TYPE_BF16) {
+        return false;
+    }
+    dst.resize((size_t) H * ch * P);
+    for (int hh = 0; hh < H; hh++) {
+        for (int cc = 0; cc < ch; cc++) {
+            for (int p = 0; p < P; p++) {
+                const float v = rd((int64_t) hh * P * ch + (int64_t) cc * P + p);
+                if (out_side) {
+                    dst[((size_t) p * ch + cc) * H + hh] = v;
+                } else {
+                    dst[(size_t) hh * ch * P + (size_t) p * ch + cc] = v;
+                }
+            }
+        }
+    }
+    return true;
+}
+
+}  // namespace
+
+extern "C" acb_status acb_dit_load(const char * gguf_path, int device, acb_dit ** out) {
+    if (!gguf_path || !out) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        set_last_error("cannot select CUDA device");
+        return ACB_ERR_CUDA;
+    }
+    GGUFFile gf;
+    if (!gf.open(gguf_path)) {
+        set_last_error(gf.error());
+        return gf.error().rfind("cannot open", 0) == 0 ? ACB_ERR_IO : ACB_ERR_FORMAT;
+    }
+    std::unique_ptr<acb_dit> m(new acb_dit());
+    m->device         = device;
+    acb_dit_config & c = m->c;
+    c.n_layers          = (int) gf.get_u32("acestep-dit.block_count");
+    c.hidden_size       = (int) gf.get_u32("acestep-dit.embedding_length");
+    c.intermediate_size = (int) gf.get_u32("acestep-dit.feed_forward_length");
+    c.n_heads           = (int) gf.get_u32("acestep-dit.attention.head_count");
+    c.n_kv_heads        = (int) gf.get_u32("acestep-dit.attention.head_count_kv");
+    c.head_dim          = (int) gf.get_u32("acestep-dit.attention.key_length");
+    c.in_channels       = (int) gf.get_u32("acestep.in_channels");
+    c.out_channels      = (int) gf.get_u32("acestep.audio_acoustic_hidden_dim");
+    c.patch_size        = (int) gf.get_u32("acestep.patch_size");
+    c.sliding_window    = (int) gf.get_u32("acestep.sliding_window");
+    c.rope_theta        = gf.get_f32("acestep-dit.rope.freq_base");
+    c.rms_norm_eps      = gf.get_f32("acestep-dit.attention.layer_norm_rms_epsilon");
+    auto bad = [&](acb_status s, const std::string & msg) {
+        set_last_error(msg);
+        return s;
+    };
+    // dit.h:289-296: every field must be present
+    if (!c.n_layers || !c.hidden_size || !c.intermediate_size || !c.n_heads || !c.n_kv_heads || !c.head_dim ||
+        !c.in_channels || !c.out_channels || !c.patch_size || !c.sliding_window || c.rope_theta <= 0.0f ||
+        c.rms_norm_eps <= 0.0f) {
+        return bad(ACB_ERR_FORMAT, "incomplete DiT config in GGUF");
+    }
+    const int H = c.hidden_size, F = c.intermediate_size, D = c.head_dim;
+    if (D != 128 || c.n_heads % c.n_kv_heads != 0 || H % 256 != 0 || F % 256 != 0 || c.n_layers > 128 ||
+        (c.in_channels * c.patch_size) % 64 != 0 || c.out_channels <= 0 || c.in_channels <= c.out_channels) {
+        return bad(ACB_ERR_UNSUPPORTED, "unsupported DiT configuration");
+    }
+    if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess) {
+        return bad(ACB_ERR_CUDA, "stream creation failed");
+    }
+
+    WeightArena & A     = m->arena;
+    auto          stage = std::make_unique<WeightArena>();
+    auto          req   = [&](DevTensor * t) { return t != nullptr; };
+    bool          ok    = true;
+    // timestep embedders
+    struct TembRaw {
+        DevTensor *l1 = nullptr, *l2 = nullptr, *tp = nullptr;
+    } tr[2];
+    for (int r = 0; r < 2; r++) {
+        const std::string p = r == 0 ? "decoder.time_embed" : "decoder.time_embed_r";
+        TembW &           E = r == 0 ? m->te : m->te_r;
+        tr[r].l1            = stage->load(gf, p + ".linear_1.weight");
+        tr[r].l2            = stage->load(gf, p + ".linear_2.weight");
+        tr[r].tp            = stage->load(gf, p + ".time_proj.weight");
+        E.b1                = A.load_f32(gf, p + ".linear_1.bias");
+        E.b2                = A.load_f32(gf, p + ".linear_2.bias");
+        E.btp               = A.load_f32(gf, p + ".time_proj.bias");
+        ok = ok && req(tr[r].l1) && req(tr[r].l2) && req(tr[r].tp) && req(E.b1) && req(E.b2) && req(E.btp);
+    }
+    // proj_in / proj_out, pre-permuted on the host
+    const int          P = c.patch_size, in_ch = c.in_channels, Oc = c.out_channels;
+    std::vector<float> pin, pout;
+    if (!conv_to_f32(gf, "decoder.proj_in.1.weight", H, in_ch, P, false, pin) ||
+        !conv_to_f32(gf, "decoder.proj_out.1.weight", H, Oc, P, true, pout)) {
+        return bad(ACB_ERR_FORMAT, "decoder.proj_in / proj_out weight missing or of an unsupported type");
+    }
+    DevTensor * pin_t  = stage->add_host(ACB_TYPE_F32, (int64_t) in_ch * P, H, pin.data(), pin.size() * 4);
+    DevTensor * pout_t = stage->add_host(ACB_TYPE_F32, H, (int64_t) Oc * P, pout.data(), pout.size() * 4);
+    m->proj_in_b       = A.load_f32(gf, "decoder.proj_in.1.bias");
+    DevTensor * pob    = A.load_f32(gf, "decoder.proj_out.1.bias");
+    DevTensor * cond_w = stage->load(gf, "decoder.condition_embedder.weight");
+    m->cond_b          = A.load_f32(gf, "decoder.condition_embedder.bias");
+    m->norm_out        = A.load_f32(gf, "decoder.norm_out.weight");
+    m->oss             = A.load_f32(gf, "decoder.scale_shift_table");
+    m->null_emb        = gf.find("null_condition_emb") ? A.load_f32(gf, "null_condition_emb") : nullptr;
+    ok = ok && req(m->proj_in_b) && req(pob) && req(cond_w) && req(m->cond_b) && req(m->norm_out) && req(m->oss);
+    if (!ok) {
+        return bad(ACB_ERR_FORMAT, !A.error.empty() ? A.error : stage->error);
+    }
+    c.enc_hidden_size = (int) cond_w->K;
+    if (cond_w->N != H || pob->K * pob->N != Oc || m->oss->K * m->oss->N != 2 * H || c.enc_hidden_size % 256 != 0) {
+        return bad(ACB_ERR_FORMAT, "DiT input/output tensor shapes do not match the config");
+    }
+    // layers
+    struct LRaw {
+        std::vector<DevTensor *> sa_qkv, ca_q, ca_kv, gu;
+        DevTensor *              sa_o = nullptr, *ca_o = nullptr, *down = nullptr, *sst = nullptr;
+    };
+    std::vector<LRaw> raw((size_t) c.n_layers);
+    m->layers.resize((size_t) c.n_layers);
+    const int QD = c.n_heads * D, KD = c.n_kv_heads * D;
+    for (int i = 0; i < c.n_layers; i++) {
+        const std::string p = "decoder.layers." + std::to_string(i);
+        DiTLayerW &       L = m->layers[(size_t) i];
+        LRaw &            R = raw[(size_t) i];
+        L.sa_norm           = A.load_f32(gf, p + ".self_attn_norm.weight");
+        L.sa_q_norm         = A.load_f32(gf, p + ".self_attn.q_norm.weight");
+        L.sa_k_norm         = A.load_f32(gf, p + ".self_attn.k_norm.weight");
+        L.ca_norm           = A.load_f32(gf, p + ".cross_attn_norm.weight");
+        L.ca_q_norm         = A.load_f32(gf, p + ".cross_attn.q_norm.weight");
+        L.ca_k_norm         = A.load_f32(gf, p + ".cross_attn.k_norm.weight");
+        L.mlp_norm          = A.load_f32(gf, p + ".mlp_norm.weight");
+        R.sst               = stage->load_f32(gf, p + ".scale_shift_table");
+        R.sa_qkv = { stage->load(gf, p + ".self_attn.q_proj.weight"), stage->load(gf, p + ".self_attn.k_proj.weight"),
+                     stage->load(gf, p + ".self_attn.v_proj.weight") };
+        R.sa_o   = stage->load(gf, p + ".self_attn.o_proj.weight");
+        R.ca_q   = { stage->load(gf, p + ".cross_attn.q_proj.weight") };
+        R.ca_kv  = { stage->load(gf, p + ".cross_attn.k_proj.weight"), stage->load(gf, p + ".cross_attn.v_proj.weight") };
+        R.ca_o   = stage->load(gf, p + ".cross_attn.o_proj.weight");
+        R.gu     = { stage->load(gf, p + ".mlp.gate_proj.weight"), stage->load(gf, p + ".mlp.up_proj.weight") };
+        R.down   = stage->load(gf, p + ".mlp.down_proj.weight");
+        bool lok = L.sa_norm && L.sa_q_norm && L.sa_k_norm && L.ca_norm && L.ca_q_norm && L.ca_k_norm && L.mlp_norm &&
+                   R.sst && R.sa_o && R.ca_o && R.down;
+        for (auto * v : { &R.sa_qkv, &R.ca_q, &R.ca_kv, &R.gu }) {
+            for (DevTensor * t : *v) {
+                lok = lok && t && t->K == H;
+            }
+        }
+        if (!lok) {
+            return bad(ACB_ERR_FORMAT, !A.error.empty()      ? A.error :
+                                       !stage->error.empty() ? stage->error :
+                                                               "missing or misshapen DiT layer tensor");
+        }
+        if (R.sa_qkv[0]->N != QD || R.sa_qkv[1]->N != KD || R.sa_qkv[2]->N != KD || R.ca_q[0]->N != QD ||
+            R.ca_kv[0]->N != KD || R.ca_kv[1]->N != KD || R.gu[0]->N != F || R.gu[1]->N != F || R.sa_o->K != QD ||
+            R.sa_o->N != H || R.ca_o->K != QD || R.ca_o->N != H || R.down->K != F || R.down->N != H ||
+            R.sst->K * R.sst->N != 6 * H || L.sa_q_norm->K != D) {
+            return bad(ACB_ERR_FORMAT, "DiT layer tensor shapes do not match the config");
+        }
+    }
+    ACB_TRY(A.upload(m->st));
+    ACB_TRY(stage->upload(m->st));
+
+    // proj_out bias repeated over the patch positions (ggml_add broadcast of [out_ch] over out_ch*P)
+    {
+        if (m->proj_out_b.alloc((size_t) Oc * P * 4, false) != ACB_OK) {
+            return bad(ACB_ERR_OOM, "bias allocation failed");
+        }
+        for (int p = 0; p < P; p++) {
+            cudaMemcpy(m->proj_out_b.as<float>() + p * Oc, pob->data, (size_t) Oc * 4, cudaMemcpyDeviceToDevice);
+        }
+        if (m->sst.alloc((size_t) c.n_layers * 6 * H * 4, false) != ACB_OK) {
+            return bad(ACB_ERR_OOM, "modulation table allocation failed");
+        }
+        for (int i = 0; i < c.n_layers; i++) {
+            cudaMemcpy(m->sst.as<float>() + (size_t) i * 6 * H, raw[(size_t) i].sst->data, (size_t) 6 * H * 4,
+                       cudaMemcpyDeviceToDevice);
+        }
+    }
+
+    // 16-bit copies of every linear
+    std::vector<std::pair<DenseLinear *, std::vector<DevTensor *>>> lins;
+    for (int r = 0; r < 2; r++) {
+        TembW & E = r == 0 ? m->te : m->te_r;
+        lins.push_back({ &E.l1, { tr[r].l1 } });
+        lins.push_back({ &E.l2, { tr[r].l2 } });
+        lins.push_back({ &E.tp, { tr[r].tp } });
+    }
+    lins.push_back({ &m->proj_in, { pin_t } });
+    lins.push_back({ &m->proj_out, { pout_t } });
+    lins.push_back({ &m->cond, { cond_w } });
+    for (int i = 0; i < c.n_layers; i++) {
+        DiTLayerW & L = m->layers[(size_t) i];
+        LRaw &      R = raw[(size_t) i];
+        lins.push_back({ &L.sa_qkv, R.sa_qkv });
+        lins.push_back({ &L.sa_o, { R.sa_o } });
+        lins.push_back({ &L.ca_q, R.ca_q });
+        lins.push_back({ &L.ca_kv, R.ca_kv });
+        lins.push_back({ &L.ca_o, { R.ca_o } });
+        lins.push_back({ &L.gu, R.gu });
+        lins.push_back({ &L.down, { R.down } });
+    }
+    size_t  total = 0;
+    int64_t max_rows = 0, max_elems = 0;
+    for (auto & lp : lins) {
+        total += (DenseLinear::elems(lp.second) * 2 + 255) & ~size_t(255);
+        for (DevTensor * t : lp.second) {
+            max_rows  = std::max(max_rows, t->N);
+            max_elems = std::max(max_elems, t->N * t->K);
+        }
+    }
+    DevBuf idbuf, tmp;
+    if (m->w16.alloc(total, false) != ACB_OK || idbuf.alloc((size_t) max_rows * 4, false) != ACB_OK ||
+        tmp.alloc((size_t) max_elems * 4, false) != ACB_OK) {
+        return bad(ACB_ERR_OOM, "16-bit weight allocation failed");
+    }
+    {
+        std::vector<int32_t> idv((size_t) max_rows);
+        for (int64_t r = 0; r < max_rows; r++) {
+            idv[(size_t) r] = (int32_t) r;
+        }
+        cudaMemcpy(idbuf.p, idv.data(), idv.size() * 4, cudaMemcpyHostToDevice);
+    }
+    uint8_t * wp = m->w16.as<uint8_t>();
+    for (auto & lp : lins) {
+        ACB_TRY(dense_build(*lp.first, lp.second, reinterpret_cast<uint16_t *>(wp), idbuf.as<int32_t>(),
+                            tmp.as<float>(), m->st));
+        wp += (DenseLinear::elems(lp.second) * 2 + 255) & ~size_t(255);
+        if (cudaStreamSynchronize(m->st) != cudaSuccess) {  // tmp is reused by the next matrix
+            return bad(ACB_ERR_CUDA, "weight conversion failed");
+        }
+    }
+    stage.reset();
+    c.has_null_condition = m->null_emb ? 1 : 0;
+    *out                 = m.release();
+    return ACB_OK;
+}
+
+// ---- C ABI ---------------------------------------------------------------------------------------
+
+extern "C" acb_status acb_dit_get_config(const acb_dit * m, acb_dit_config * cfg) {
+    if (!m || !cfg) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    *cfg = m->c;
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_dit_set_exact(acb_dit * m, int exact) {
+    if (!m) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (m->exact != (exact != 0)) {
+        m->exact = exact != 0;
+        m->drop_graphs();
+    }
+    return ACB_OK;
+}
+
+extern "C" size_t acb_dit_weight_bytes(const acb_dit * m) {
+    return m ? m->arena.bytes() + m->w16.bytes : 0;
+}
+
+extern "C" acb_status acb_dit_forward(acb_dit * m, const float * d_input, const float * d_enc, int N, int T, int enc_S,
+                                      float t, float t_r, float * d_velocity, int n_layers_run, acb_stream_t stream) {
+    if (!m || !d_input || !d_enc || !d_velocity || N <= 0 || T <= 0 || enc_S <= 0 || T % m->c.patch_size != 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->reserve(N, T, enc_S));
+    cudaStream_t  s  = (cudaStream_t) stream;
+    const float   tv[3] = { t, t_r, 0.0f };
+    const size_t  nin = (size_t) N * T * m->c.in_channels * 4;
+    const size_t  nen = (size_t) N * enc_S * m->c.enc_hidden_size * 4;
+    if (cudaMemcpyAsync(m->tt.p, tv, sizeof(tv), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->input.p, d_input, nin, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->enc_in.p, d_enc, nen, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->condition(s));
+    ACB_TRY(m->evaluate(n_layers_run, s));
+    const size_t nv = (size_t) N * T * m->c.out_channels * 4;
+    if (cudaMemcpyAsync(d_velocity, m->vel.p, nv, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    // tt must outlive the async copy: synchronise before returning the stack array
+    return cudaStreamSynchronize(s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
+}
+
+extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
+                                       const float * enc_hidden, int enc_S, int T, int N, int num_steps,
+                                       const float * schedule, float * output, float guidance_scale, float * gpu_ms) {
+    if (!m || !noise || !context_latents || !enc_hidden || !schedule || !output || N <= 0 || T <= 0 || enc_S <= 0 ||
+        num_steps <= 0 || T % m->c.patch_size != 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    const acb_dit_config & c      = m->c;
+    const int              Oc     = c.out_channels;
+    const int              in_ch  = c.in_channels, ctx_ch = in_ch - Oc;
+    const int              He     = c.enc_hidden_size;
+    // CFG batching (dit-sampler.h:167-171): conditional slots [0, N), unconditional [N, 2N)
+    const bool do_cfg = guidance_scale > 1.0f && m->null_emb;
+    const int  Ng     = do_cfg ? 2 * N : N;
+    ACB_TRY(m->reserve(Ng, T, enc_S));
+    cudaStream_t s     = m->st;
+    const size_t n_per = (size_t) T * Oc, n_tot = n_per * N;
+    bool         bad   = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
+                 m->ra.bytes < n_tot * 8;
+    if (bad) {
+        m->drop_graphs();  // the graphs hold these addresses
+        if (m->xt.alloc(n_tot * 4) != ACB_OK || m->vt.alloc(n_tot * 4) != ACB_OK || m->out.alloc(n_tot * 4) != ACB_OK ||
+            m->ra.alloc(n_tot * 8) != ACB_OK) {
+            set_last_error("DiT generate buffers allocation failed");
+            return ACB_ERR_OOM;
+        }
+    }
+    // inputs: context channels of every slot (uncond mirrors cond), the noise, the condition
+    {
+        std::vector<float> in((size_t) Ng * T * in_ch, 0.0f);
+        for (int b = 0; b < Ng; b++) {
+            const int src = b % N;
+            for (int t = 0; t < T; t++) {
+                memcpy(&in[((size_t) b * T + t) * in_ch], &context_latents[((size_t) src * T + t) * ctx_ch],
+                       (size_t) ctx_ch * 4);
+            }
+        }
+        std::vector<float> enc((size_t) Ng * enc_S * He);
+        memcpy(enc.data(), enc_hidden, (size_t) N * enc_S * He * 4);
+        if (do_cfg) {
+            // null_condition_emb broadcast over enc_S rows for the unconditional slots (:345-385)
+            std::vector<float> nul((size_t) He);
+            if (m->null_emb->type == ACB_TYPE_F32 && m->null_emb->K * m->null_emb->N == He) {
+                cudaMemcpy(nul.data(), m->null_emb->data, (size_t) He * 4, cudaMemcpyDeviceToHost);
+            } else {
+                set_last_error("null_condition_emb has an unexpected shape");
+                return ACB_ERR_FORMAT;
+            }
+            for (int b = N; b < Ng; b++) {
+                for (int r = 0; r < enc_S; r++) {
+                    memcpy(&enc[((size_t) b * enc_S + r) * He], nul.data(), (size_t) He * 4);
+                }
+            }
+        }
+        if (cudaMemcpyAsync(m->input.p, in.data(), in.size() * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(m->enc_in.p, enc.data(), enc.size() * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaMemcpyAsync(m->xt.p, noise, n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+    }
+    ACB_TRY(m->condition(s));
+
+    // one graph per (shape, cfg, first, last): pack xt, evaluate, guidance, Euler / x0
+    auto get_graph = [&](int first, int last, cudaGraphExec_t * ex) -> acb_status {
+        uint32_t gbits = 0;  // the guidance scale is baked into the captured APG launch
+        memcpy(&gbits, &guidance_scale, 4);
+        const auto key =
+            std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, first * 2 + last, m->exact ? 1 : 0, gbits);
+        auto       it  = m->graphs.find(key);
+        if (it != m->graphs.end()) {
+            *ex = it->second;
+            return ACB_OK;
+        }
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        acb_status st = acb_dit_pack_xt(m->xt.as<float>(), m->input.as<float>(), N, Ng, T, Oc, ctx_ch, (acb_stream_t) s);
+        if (st == ACB_OK) {
+            st = m->evaluate(-1, s);
+        }
+        float * v = m->vel.as<float>();
+        if (st == ACB_OK && do_cfg) {
+            st = acb_dit_apg(v, v + n_tot, m->ra.as<double>(), first, -0.75f, guidance_scale, 2.5f, N, T, Oc,
+                             m->vt.as<float>(), (acb_stream_t) s);
+            v  = m->vt.as<float>();
+        }
+        if (st == ACB_OK) {
+            st = acb_dit_euler(m->xt.as<float>(), v, m->tt.as<float>(), last, m->out.as<float>(), (int64_t) n_tot,
+                               (acb_stream_t) s);
+        }
+        const cudaError_t ce = cudaStreamEndCapture(s, &g);
+        if (st != ACB_OK || ce != cudaSuccess) {
+            if (g) {
+                cudaGraphDestroy(g);
+            }
+            set_last_error("DiT step graph capture failed");
+            return st != ACB_OK ? st : ACB_ERR_CUDA;
+        }
+        const cudaError_t ie = cudaGraphInstantiate(ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        m->graphs.emplace(key, *ex);
+        return ACB_OK;
+    };
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    acb_status st = ACB_OK;
+    std::vector<float> tv((size_t) num_steps * 3);
+    for (int step = 0; step < num_steps && st == ACB_OK; step++) {
+        const int       first = step == 0, last = step == num_steps - 1;
+        cudaGraphExec_t ex    = nullptr;
+        st                    = get_graph(first, last, &ex);
+        if (st != ACB_OK) {
+            break;
+        }
+        // t_curr, t_r = t_curr (dit-sampler.h:431-436), t_next
+        float * t3 = &tv[(size_t) step * 3];
+        t3[0]      = schedule[step];
+        t3[1]      = schedule[step];
+        t3[2]      = last ? 0.0f : schedule[step + 1];
+        if (step == 0) {
+            cudaEventRecord(e0, s);
+        }
+        if (cudaMemcpyAsync(m->tt.p, t3, 3 * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaGraphLaunch(ex, s) != cudaSuccess) {
+            st = ACB_ERR_CUDA;
+        }
+    }
+    cudaEventRecord(e1, s);
+    int dev_err = 0;
+    if (st == ACB_OK && (cudaMemcpyAsync(output, m->out.p, n_tot * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                         cudaMemcpyAsync(&dev_err, m->err.p, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                         cudaStreamSynchronize(s) != cudaSuccess)) {
+        st = ACB_ERR_CUDA;
+    }
+    if (st == ACB_OK && gpu_ms) {
+        cudaEventElapsedTime(gpu_ms, e0, e1);
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (st == ACB_OK && dev_err) {
+        set_last_error("device error flag " + std::to_string(dev_err));
+        return ACB_ERR_DEVICE;
+    }
+    return st;
+}
+
+extern "C" void acb_dit_free(acb_dit * m) {
+    delete m;
+}

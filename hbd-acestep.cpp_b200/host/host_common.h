@@ -5,6 +5,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstdint>
 #include <cstring>
 #include <string>
 
@@ -21,6 +22,33 @@ void set_last_error(const std::string & e);
             return s_;             \
         }                          \
     } while (0)
+
+// IEEE binary16 / bfloat16 storage to float (exact).
+inline float host_bf16_to_f32(uint16_t h) {
+    const uint32_t u = (uint32_t) h << 16;
+    float          f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+inline float host_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t) (h & 0x8000) << 16;
+    const uint32_t exp  = (h >> 10) & 0x1f;
+    const uint32_t man  = h & 0x3ff;
+    uint32_t       u;
+    if (exp == 0) {
+        const float v = (float) man * 5.9604644775390625e-8f;  // subnormal: man * 2^-24
+        return sign ? -v : v;
+    }
+    if (exp == 31) {
+        u = sign | 0x7f800000u | (man << 13);
+    } else {
+        u = sign | ((exp + 112) << 23) | (man << 13);
+    }
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
 
 // Value text of "key": in a flat JSON object (the lookup of qw3lm_json_int / _float / _bool,
 // src/qwen3-lm.h:60-121), or nullptr.

@@ -3,33 +3,9 @@
 
 #include <cstring>
 
+#include "host_common.h"
+
 namespace acb {
-
-static float bf16_to_f32(uint16_t h) {
-    uint32_t u = (uint32_t) h << 16;
-    float    f;
-    memcpy(&f, &u, 4);
-    return f;
-}
-
-static float f16_to_f32(uint16_t h) {
-    const uint32_t sign = (uint32_t) (h & 0x8000) << 16;
-    const uint32_t exp  = (h >> 10) & 0x1f;
-    const uint32_t man  = h & 0x3ff;
-    uint32_t       u;
-    if (exp == 0) {
-        float v = (float) man * 5.9604644775390625e-8f;
-        return sign ? -v : v;
-    }
-    if (exp == 31) {
-        u = sign | 0x7f800000u | (man << 13);
-    } else {
-        u = sign | ((exp + 112) << 23) | (man << 13);
-    }
-    float f;
-    memcpy(&f, &u, 4);
-    return f;
-}
 
 WeightArena::~WeightArena() {
     if (base_) {
@@ -95,7 +71,7 @@ DevTensor * WeightArena::load_f32(const GGUFFile & gf, const std::string & name)
     std::unique_ptr<float[]> buf(new float[n]);
     const uint16_t *         p = (const uint16_t *) s->data;
     for (size_t i = 0; i < n; i++) {
-        buf[i] = s->type == ACB_TYPE_BF16 ? bf16_to_f32(p[i]) : f16_to_f32(p[i]);
+        buf[i] = s->type == ACB_TYPE_BF16 ? host_bf16_to_f32(p[i]) : host_f16_to_f32(p[i]);
     }
     DevTensor * t = reserve(ACB_TYPE_F32, K, N, n * 4);
     pending_.push_back({ t, buf.get(), n * 4, 0 });

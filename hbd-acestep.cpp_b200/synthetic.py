@@ -110,3 +110,112 @@ def write_lm_gguf(path: str, cfg: dict, policy=policy_q8_0, seed: int = 0, devic
     w.write_tensors_to_file()
     w.close()
     return total
+
+
+# ---- DiT (src/dit.h) ---------------------------------------------------------------------------
+
+ACESTEP_DIT_2B = dict(n_layers=24, hidden_size=2048, intermediate_size=6144, n_heads=16, n_kv_heads=8, head_dim=128,
+                      in_channels=192, out_channels=64, patch_size=2, sliding_window=128, rope_theta=1000000.0,
+                      rms_norm_eps=1e-6, enc_hidden_size=2048)
+
+
+def dit_tensors(cfg: dict, qtype: int = Q8_0, seed: int = 0, device: str = "cuda", null_condition: bool = True):
+    """Yields (name, qtype, raw, K, shape) of a DiT GGUF in file order, the reference's names and
+    the quantize tool's choices (tools/quantize.cpp:97-125): 2-D linears in `qtype`, norms,
+    biases, scale_shift_table and null_condition_emb F32, the conv proj_in / proj_out BF16 (their
+    innermost dimension, the patch size, is not a block multiple). raw is uint8 [N, row_bytes]
+    for quantised tensors, float32 / bf16 bits otherwise; shape is the numpy (PyTorch) shape."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["n_layers"]
+    Nh, Nkv, D = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
+    in_ch, oc, P, He = cfg["in_channels"], cfg["out_channels"], cfg["patch_size"], cfg["enc_hidden_size"]
+
+    def mat(name, N, K, std=0.02):
+        w = torch.randn((N, K), generator=g, device=device) * std
+        return name, qtype, quantize_on_device(w, qtype), K, (N, K)
+
+    def vec(name, shape, base=0.0, std=0.02):
+        v = (base + std * torch.randn(shape, generator=g, device=device)).cpu().numpy().astype(np.float32)
+        return name, F32, v, shape[-1], shape
+
+    def conv_bf16(name, shape):
+        w = (torch.randn(shape, generator=g, device=device) * 0.02).to(torch.bfloat16)
+        return name, acb.BF16, w.view(torch.int16).cpu().numpy().view(np.uint16), shape[-1], shape
+
+    for te in ("decoder.time_embed", "decoder.time_embed_r"):
+        yield mat(f"{te}.linear_1.weight", H, 256)
+        yield vec(f"{te}.linear_1.bias", (H,))
+        yield mat(f"{te}.linear_2.weight", H, H)
+        yield vec(f"{te}.linear_2.bias", (H,))
+        yield mat(f"{te}.time_proj.weight", 6 * H, H)
+        yield vec(f"{te}.time_proj.bias", (6 * H,))
+    yield conv_bf16("decoder.proj_in.1.weight", (H, in_ch, P))
+    yield vec("decoder.proj_in.1.bias", (H,))
+    yield mat("decoder.condition_embedder.weight", H, He)
+    yield vec("decoder.condition_embedder.bias", (H,))
+    for i in range(L):
+        p = f"decoder.layers.{i}"
+        yield vec(f"{p}.self_attn_norm.weight", (H,), 1.0, 0.01)
+        yield mat(f"{p}.self_attn.q_proj.weight", Nh * D, H)
+        yield mat(f"{p}.self_attn.k_proj.weight", Nkv * D, H)
+        yield mat(f"{p}.self_attn.v_proj.weight", Nkv * D, H)
+        yield mat(f"{p}.self_attn.o_proj.weight", H, Nh * D)
+        yield vec(f"{p}.self_attn.q_norm.weight", (D,), 1.0, 0.01)
+        yield vec(f"{p}.self_attn.k_norm.weight", (D,), 1.0, 0.01)
+        yield vec(f"{p}.cross_attn_norm.weight", (H,), 1.0, 0.01)
+        yield mat(f"{p}.cross_attn.q_proj.weight", Nh * D, H)
+        yield mat(f"{p}.cross_attn.k_proj.weight", Nkv * D, H)
+        yield mat(f"{p}.cross_attn.v_proj.weight", Nkv * D, H)
+        yield mat(f"{p}.cross_attn.o_proj.weight", H, Nh * D)
+        yield vec(f"{p}.cross_attn.q_norm.weight", (D,), 1.0, 0.01)
+        yield vec(f"{p}.cross_attn.k_norm.weight", (D,), 1.0, 0.01)
+        yield vec(f"{p}.mlp_norm.weight", (H,), 1.0, 0.01)
+        yield mat(f"{p}.mlp.gate_proj.weight", F, H)
+        yield mat(f"{p}.mlp.up_proj.weight", F, H)
+        yield mat(f"{p}.mlp.down_proj.weight", H, F)
+        yield vec(f"{p}.scale_shift_table", (1, 6, H), 0.0, 0.05)
+    yield vec("decoder.norm_out.weight", (H,), 1.0, 0.01)
+    yield vec("decoder.scale_shift_table", (1, 2, H), 0.0, 0.05)
+    yield conv_bf16("decoder.proj_out.1.weight", (H, oc, P))
+    yield vec("decoder.proj_out.1.bias", (oc,))
+    if null_condition:
+        yield vec("null_condition_emb", (He,), 0.0, 1.0)
+
+
+def write_dit_gguf(path: str, cfg: dict, qtype: int = Q8_0, seed: int = 0, device: str = "cuda",
+                   keep: dict | None = None, null_condition: bool = True) -> int:
+    """Write a DiT GGUF with the reference's metadata keys (dit.h:276-287). If `keep` is a dict,
+    the raw tensors are stored in it as name -> (qtype, raw, K, shape)."""
+    import gguf
+    w = gguf.GGUFWriter(path, "acestep-dit")
+    a = "acestep-dit"
+    w.add_uint32(f"{a}.block_count", cfg["n_layers"])
+    w.add_uint32(f"{a}.embedding_length", cfg["hidden_size"])
+    w.add_uint32(f"{a}.feed_forward_length", cfg["intermediate_size"])
+    w.add_uint32(f"{a}.attention.head_count", cfg["n_heads"])
+    w.add_uint32(f"{a}.attention.head_count_kv", cfg["n_kv_heads"])
+    w.add_uint32(f"{a}.attention.key_length", cfg["head_dim"])
+    w.add_float32(f"{a}.rope.freq_base", cfg["rope_theta"])
+    w.add_float32(f"{a}.attention.layer_norm_rms_epsilon", cfg["rms_norm_eps"])
+    w.add_uint32("acestep.in_channels", cfg["in_channels"])
+    w.add_uint32("acestep.audio_acoustic_hidden_dim", cfg["out_channels"])
+    w.add_uint32("acestep.patch_size", cfg["patch_size"])
+    w.add_uint32("acestep.sliding_window", cfg["sliding_window"])
+    total = 0
+    for name, qt, raw, K, shape in dit_tensors(cfg, qtype, seed, device, null_condition):
+        if qt == F32:
+            w.add_tensor(name, raw)
+        elif qt == acb.BF16:
+            w.add_tensor(name, raw.view(np.uint8).reshape(*shape[:-1], shape[-1] * 2),
+                         raw_dtype=gguf.GGMLQuantizationType.BF16)
+        else:
+            w.add_tensor(name, raw, raw_dtype=gguf.GGMLQuantizationType(qt))
+        total += raw.nbytes
+        if keep is not None:
+            keep[name] = (qt, raw, K, shape)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return total

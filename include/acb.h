@@ -182,7 +182,8 @@ ACB_API acb_status acb_act_quant_ex(const float * x, int64_t x_stride, int64_t u
                                     int64_t lo_offset, acb_stream_t stream);
 
 /* Vec-dot type of a weight type (ggml's type_traits_cpu[].vec_dot_type): Q8_0 for Q8_0, Q8_K
- * for Q4_K / Q6_K, the type itself for F16 / BF16; -1 for types without a tensor-core path. */
+ * for Q4_K / Q6_K, the type itself for F16 / BF16 / F32 (F32: the activation stays f32; the
+ * exact layouts split it, a plain operand rounds it to f16); -1 for other types. */
 ACB_API int acb_vec_dot_type(int weight_type);
 
 /* C[m][n] = epi(sum_k A[m][k] B[n][k]) on the 5th-generation tensor cores (tcgen05.mma, TMEM
@@ -241,6 +242,33 @@ ACB_API acb_status acb_attn_prefill_split(const void * q, int64_t q_bs, int64_t 
                                           int o_type, int64_t o_bs, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
                                           int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
                                           int flags, int64_t q_lo, int64_t k_lo, int64_t v_lo, acb_stream_t stream);
+
+/* ---- DiT step kernels (configs 4 and 5) ------------------------------------------------------ */
+
+/* tt = {t, t_r} on the device: out[0][:] = ggml_timestep_embedding(t*1000, dim, max_period),
+ * out[1][:] = the same of (t - t_r)*1000 (dit_ggml_build_temb, src/dit-graph.h:81-117). */
+ACB_API acb_status acb_dit_sinusoid(const float * tt, int dim, int max_period, float * out, acb_stream_t stream);
+/* y = x / (1 + exp(-x)) (ggml_silu). */
+ACB_API acb_status acb_silu(const float * x, float * y, int64_t n, acb_stream_t stream);
+/* Modulation vectors of one step (src/dit-graph.h:383-400, 591-606): ada[l] = sst[l] +
+ * (tproj2[0] + tproj2[1]) for each layer's six [H] vectors (sst [n_layers][6H]); out_ss[0] =
+ * oss[0] + (temb2[0] + temb2[1]) (shift), out_ss[1] = oss[1] + ... (scale). */
+ACB_API acb_status acb_dit_modulation(const float * sst, const float * tproj2, const float * temb2, const float * oss,
+                                      int n_layers, int H, float * ada, float * out_ss, acb_stream_t stream);
+/* Noisy latent xt [N][T][Oc] into the xt channels of the DiT input [Ng][T][ctx_ch + Oc]; slot b
+ * takes sample b % N (src/dit-sampler.h:466-479). */
+ACB_API acb_status acb_dit_pack_xt(const float * xt, float * input, int N, int Ng, int T, int Oc, int ctx_ch,
+                                   acb_stream_t stream);
+/* APG guidance (apg_forward, src/dit-sampler.h:73-122) for N samples [T][Oc] in double:
+ * running_avg [N][T][Oc] doubles (first != 0 starts it), momentum -0.75 and norm threshold 2.5
+ * in the reference. vt = cond + (guidance_scale - 1) * orthogonal part. */
+ACB_API acb_status acb_dit_apg(const float * cond, const float * uncond, double * running_avg, int first,
+                               float momentum, float guidance_scale, float norm_threshold, int N, int T, int Oc,
+                               float * vt, acb_stream_t stream);
+/* tt = {t_curr, t_r, t_next}: xt -= vt * (t_curr - t_next) (solver-euler.h:8-18), or with last != 0
+ * out = xt - vt * t_curr (the x0 prediction, dit-sampler.h:596-604). */
+ACB_API acb_status acb_dit_euler(float * xt, const float * vt, const float * tt, int last, float * out, int64_t n,
+                                 acb_stream_t stream);
 
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 

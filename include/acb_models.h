@@ -89,6 +89,59 @@ ACB_API acb_status acb_qwen3_forward_hidden(acb_qwen3_enc * m, const float * d_h
 ACB_API acb_status acb_qwen3_embed_lookup(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output);
 ACB_API void       acb_qwen3_free(acb_qwen3_enc * m); /* qwen3_free :483 */
 
+/* ---- ACE-Step DiT (replaces src/dit.h, src/dit-graph.h, src/dit-sampler.h) ------------------- */
+
+typedef struct acb_dit acb_dit;
+
+/* DiTGGMLConfig (dit.h) from the GGUF keys acestep-dit.* / acestep.*, plus the condition width
+ * (condition_embedder input) and whether null_condition_emb (CFG) is present. */
+typedef struct {
+    int   n_layers;
+    int   hidden_size;
+    int   intermediate_size;
+    int   n_heads;
+    int   n_kv_heads;
+    int   head_dim;
+    int   in_channels;
+    int   out_channels;
+    int   patch_size;
+    int   sliding_window;
+    float rope_theta;
+    float rms_norm_eps;
+    int   enc_hidden_size;
+    int   has_null_condition;
+} acb_dit_config;
+
+/* dit_ggml_load (dit.h:256-420): decoder.* tensors, proj_in / proj_out pre-permuted to F32 at
+ * load, every linear dequantised once to a resident 16-bit copy ([hi|lo|hi] f16 for quantised and
+ * F32 weights, see acb_act_quant_ex) for the tensor-core GEMM. */
+ACB_API acb_status acb_dit_load(const char * gguf_path, int device, acb_dit ** out);
+ACB_API acb_status acb_dit_get_config(const acb_dit * m, acb_dit_config * cfg);
+ACB_API size_t     acb_dit_weight_bytes(const acb_dit * m);
+/* exact (default, nonzero): hi/lo split products, tracking the reference CPU build to fp32
+ * summation order at 3x tensor work; fast (0): single f16 operands. */
+ACB_API acb_status acb_dit_set_exact(acb_dit * m, int exact);
+
+/* One DiT evaluation (dit_ggml_build_graph + compute, dit-graph.h:466-619) on device buffers:
+ * input [N][T][in_channels] (context channels then xt), enc [N][enc_S][enc_hidden_size] ->
+ * velocity [N][T][out_channels]; t and t_r the two timesteps (time_embed_r sees t - t_r).
+ * n_layers_run < 0 runs every layer, else only the first n_layers_run (then the output stage).
+ * All frames and condition rows are real (no padding masks). Synchronises `stream`. */
+ACB_API acb_status acb_dit_forward(acb_dit * m, const float * d_input, const float * d_enc, int N, int T, int enc_S,
+                                   float t, float t_r, float * d_velocity, int n_layers_run, acb_stream_t stream);
+
+/* dit_ggml_generate (dit-sampler.h:132-711) with the Euler solver, host arrays as in the reference:
+ * noise [N][T][out_channels], context_latents [N][T][in_channels - out_channels], enc_hidden
+ * [N][enc_S][enc_hidden_size], schedule[num_steps] -> output [N][T][out_channels] (the x0
+ * prediction of the last step). guidance_scale > 1 with a null condition runs batched CFG
+ * (2N sequences per evaluation) with APG. Each step is one CUDA graph (captured on first use per
+ * shape); gpu_ms (optional) receives the device time of the step loop. Not covered: cover mode,
+ * padding masks (real_S / real_enc_S), DCW and the other solvers. */
+ACB_API acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
+                                    const float * enc_hidden, int enc_S, int T, int N, int num_steps,
+                                    const float * schedule, float * output, float guidance_scale, float * gpu_ms);
+ACB_API void       acb_dit_free(acb_dit * m);
+
 /* ---- Qwen3 causal LM (replaces src/qwen3-lm.h) ---------------------------------------------- */
 
 typedef struct acb_qw3lm acb_qw3lm;

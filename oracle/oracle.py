@@ -482,3 +482,106 @@ def qwen3_from_gguf_tensors(cfg, tensors, prefix="model."):
               Nkv=cfg["num_key_value_heads"], D=cfg["head_dim"], V=cfg["vocab_size"], rope_theta=cfg["rope_theta"],
               eps=cfg["rms_norm_eps"])
     return OracleQwen3(oc, w)
+
+
+def dit_from_gguf_tensors(cfg, tensors):
+    """OracleDiT over the raw tensors of a DiT GGUF {name: (qtype, raw, K, shape)} with the
+    reference's names (decoder.*): Q||K||V and gate||up concatenated by rows, proj_in / proj_out
+    pre-permuted to F32 like dit_load_proj_in_w / dit_load_proj_out_w (src/dit.h:142-252).
+    cfg uses the acb_dit_config field names."""
+    H, L = cfg["hidden_size"], cfg["n_layers"]
+    in_ch, oc, P = cfg["in_channels"], cfg["out_channels"], cfg["patch_size"]
+
+    def plain(name):
+        qt, raw, K, shape = tensors[name]
+        if qt == F32:
+            a = np.ascontiguousarray(raw, dtype=np.float32).reshape(-1)
+            return (F32, a, K, a.size // K)
+        return (qt, raw, K, shape[0])
+
+    def f32_of(name):
+        qt, raw, K, shape = tensors[name]
+        if qt == BF16:
+            return bf16_bits_to_f32(np.asarray(raw).view(np.uint16)).reshape(shape)
+        return np.asarray(raw, dtype=np.float32).reshape(shape)
+
+    def cat(names):
+        parts = [tensors[n] for n in names]
+        assert len({p[0] for p in parts}) == 1, "stacked projections of one type only"
+        return (parts[0][0], np.concatenate([p[1] for p in parts]), parts[0][2], sum(p[3][0] for p in parts))
+
+    w = {}
+    for pre, key in (("decoder.time_embed", "te"), ("decoder.time_embed_r", "te_r")):
+        w[f"{key}.l1_w"] = plain(f"{pre}.linear_1.weight")
+        w[f"{key}.l1_b"] = plain(f"{pre}.linear_1.bias")
+        w[f"{key}.l2_w"] = plain(f"{pre}.linear_2.weight")
+        w[f"{key}.l2_b"] = plain(f"{pre}.linear_2.bias")
+        w[f"{key}.tp_w"] = plain(f"{pre}.time_proj.weight")
+        w[f"{key}.tp_b"] = plain(f"{pre}.time_proj.bias")
+    pin = np.ascontiguousarray(f32_of("decoder.proj_in.1.weight").transpose(0, 2, 1).reshape(H, P * in_ch))
+    w["proj_in_w"] = (F32, pin, P * in_ch, H)
+    w["proj_in_b"] = plain("decoder.proj_in.1.bias")
+    w["cond_w"] = plain("decoder.condition_embedder.weight")
+    w["cond_b"] = plain("decoder.condition_embedder.bias")
+    for i in range(L):
+        p = f"decoder.layers.{i}"
+        w[f"layers.{i}.sa_norm"] = plain(f"{p}.self_attn_norm.weight")
+        w[f"layers.{i}.sa_qkv"] = cat([f"{p}.self_attn.{n}_proj.weight" for n in "qkv"])
+        w[f"layers.{i}.sa_q_norm"] = plain(f"{p}.self_attn.q_norm.weight")
+        w[f"layers.{i}.sa_k_norm"] = plain(f"{p}.self_attn.k_norm.weight")
+        w[f"layers.{i}.sa_o"] = plain(f"{p}.self_attn.o_proj.weight")
+        w[f"layers.{i}.ca_norm"] = plain(f"{p}.cross_attn_norm.weight")
+        w[f"layers.{i}.ca_qkv"] = cat([f"{p}.cross_attn.{n}_proj.weight" for n in "qkv"])
+        w[f"layers.{i}.ca_q_norm"] = plain(f"{p}.cross_attn.q_norm.weight")
+        w[f"layers.{i}.ca_k_norm"] = plain(f"{p}.cross_attn.k_norm.weight")
+        w[f"layers.{i}.ca_o"] = plain(f"{p}.cross_attn.o_proj.weight")
+        w[f"layers.{i}.mlp_norm"] = plain(f"{p}.mlp_norm.weight")
+        w[f"layers.{i}.gate_up"] = cat([f"{p}.mlp.gate_proj.weight", f"{p}.mlp.up_proj.weight"])
+        w[f"layers.{i}.down"] = plain(f"{p}.mlp.down_proj.weight")
+        sst = f32_of(f"{p}.scale_shift_table").reshape(-1)
+        w[f"layers.{i}.scale_shift"] = (F32, sst, H, 6)
+    w["norm_out"] = plain("decoder.norm_out.weight")
+    w["out_ss"] = (F32, f32_of("decoder.scale_shift_table").reshape(-1), H, 2)
+    pout = np.ascontiguousarray(f32_of("decoder.proj_out.1.weight").transpose(2, 1, 0).reshape(P * oc, H))
+    w["proj_out_w"] = (F32, pout, H, P * oc)
+    w["proj_out_b"] = plain("decoder.proj_out.1.bias")
+    oc_cfg = dict(n_layers=L, H=H, F=cfg["intermediate_size"], Nh=cfg["n_heads"], Nkv=cfg["n_kv_heads"],
+                  D=cfg["head_dim"], in_ch=in_ch, out_ch=oc, P=P, sliding_window=cfg["sliding_window"],
+                  H_enc=cfg["enc_hidden_size"], rope_theta=cfg["rope_theta"], eps=cfg["rms_norm_eps"])
+    return OracleDiT(oc_cfg, w)
+
+
+def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, momentum=-0.75, norm_threshold=2.5):
+    """dit_ggml_generate (src/dit-sampler.h:132-711) with the Euler solver over an OracleDiT:
+    batched CFG with APG in double when guidance_scale > 1 and a null condition is given.
+    Returns x0 [N][T][out_ch]."""
+    N, T, Oc = noise.shape
+    xt = noise.astype(np.float32).copy()
+    cfg_on = guidance_scale > 1.0 and null_emb is not None
+    ra = None
+    for step, t in enumerate(schedule):
+        x_in = np.concatenate([context, xt], axis=2).astype(np.float32)
+        if cfg_on:
+            x_in = np.concatenate([x_in, x_in])
+            e = np.concatenate([enc, np.broadcast_to(null_emb, enc.shape)]).astype(np.float32)
+        else:
+            e = enc
+        v = od.forward(x_in, e, float(t), float(t))
+        if cfg_on:
+            cond, unc = v[:N].astype(np.float64), v[N:].astype(np.float64)
+            diff = cond - unc
+            ra = diff if ra is None else diff + momentum * ra
+            n2 = (ra * ra).sum(axis=1, keepdims=True)          # per (sample, channel) over T
+            nr = np.sqrt(np.maximum(n2, 0.0))
+            s = np.where(nr > 1e-60, np.minimum(1.0, norm_threshold / np.where(nr > 1e-60, nr, 1.0)), 1.0)
+            d = np.where(s < 1.0, ra * s, ra)
+            v2 = (cond * cond).sum(axis=1, keepdims=True)
+            inv = np.where(v2 > 1e-60, 1.0 / np.sqrt(np.where(v2 > 1e-60, v2, 1.0)), 0.0)
+            dot = (d * (cond * inv)).sum(axis=1, keepdims=True)
+            orth = d - dot * (cond * inv)
+            v = (cond + (guidance_scale - 1.0) * orth).astype(np.float32)
+        if step == len(schedule) - 1:
+            return (xt - v * np.float32(t)).astype(np.float32)
+        dt = np.float32(np.float32(t) - np.float32(schedule[step + 1]))
+        xt = (xt - v * dt).astype(np.float32)
+    return xt

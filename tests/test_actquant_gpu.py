@@ -57,7 +57,7 @@ def test_vec_dot_types():
     assert acb.vec_dot_type(acb.Q8_0) == acb.Q8_0
     assert acb.vec_dot_type(acb.Q4_K) == acb.Q8_K and acb.vec_dot_type(acb.Q6_K) == acb.Q8_K
     assert acb.vec_dot_type(acb.F16) == acb.F16 and acb.vec_dot_type(acb.BF16) == acb.BF16
-    assert acb.vec_dot_type(acb.F32) == -1
+    assert acb.vec_dot_type(acb.F32) == acb.F32 and acb.vec_dot_type(acb.Q8_K) == -1
 
 
 def _split(v):
