@@ -294,6 +294,12 @@ def run_ours(args):
     if args.workloads == "gemm":
         print(json.dumps(run_gemm_shapes(dev)), flush=True)
         return
+    if args.workloads == "dit":
+        r = run_dit(dev, rank, want_cpu=not args.no_cpu_baseline)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands (Q8_0-quantised activations)")),
+                  flush=True)
+        return
     if args.workloads == "enc":
         r = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
         if rank == 0:
@@ -696,6 +702,125 @@ def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
     except OSError:
         pass
     return res
+
+
+DIT_TRACKS, DIT_T, DIT_ENC_S, DIT_STEPS, DIT_GUIDANCE = 4, 1500, 512, 8, 3.0
+
+
+def dit_step_flops(cfg, Ng, S, enc_S) -> int:
+    """Algorithmic FLOPs of one DiT evaluation over Ng sequences: every linear (2*rows*N*K; the
+    condition K/V projections counted once per step as the reference computes them) plus self
+    attention (windowed on even layers) and cross attention (QK^T and PV, 2*D flops each)."""
+    H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["n_layers"]
+    Nh, Nkv, D = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
+    R, Re = Ng * S, Ng * enc_S
+    QD, KD = Nh * D, Nkv * D
+    per_layer = 2 * R * (H * (QD + 2 * KD) + QD * H + H * QD + QD * H + H * 2 * F + F * H) + 2 * Re * H * 2 * KD
+    win = cfg["sliding_window"]
+    pairs_full = S * S
+    pairs_win = sum(min(S, i + win + 1) - max(0, i - win) for i in range(S)) if S > win else S * S
+    att = 0
+    for l in range(L):
+        att += 4 * D * Nh * Ng * (pairs_win if l % 2 == 0 else pairs_full) + 4 * D * Nh * Ng * S * enc_S
+    io = 2 * R * (cfg["in_channels"] * cfg["patch_size"] * H + H * cfg["out_channels"] * cfg["patch_size"])
+    io += 2 * Re * cfg["enc_hidden_size"] * H
+    return L * per_layer + att + io
+
+
+def run_dit(dev, rank, want_cpu=True, reps=2, modes=("exact", "fast")):
+    """Config 4 on this GPU: DiT 24 layers, 4 tracks x CFG 2 (8 sequences), 1500 frames, 512
+    condition rows, 8 turbo Euler steps with APG; steps/s of the device step loop."""
+    import tempfile
+
+    import numpy as np
+
+    import acb
+    import synthetic
+
+    cfg = dict(synthetic.ACESTEP_DIT_2B)
+    path = os.path.join(tempfile.gettempdir(), f"acb_bench_dit2b_q8_0_r{rank}.gguf")
+    keep = {} if want_cpu else None
+    t0 = time.time()
+    synthetic.write_dit_gguf(path, cfg, synthetic.Q8_0, seed=21, device=str(dev), keep=keep)
+    t_gen = time.time() - t0
+    dit = acb.DiT(path, device=dev.index or 0)
+    rng = np.random.default_rng(17)
+    N, T, enc_S, Oc = DIT_TRACKS, DIT_T, DIT_ENC_S, cfg["out_channels"]
+    noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((N, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    sched = acb.turbo_schedule(DIT_STEPS)
+    Ng, S = 2 * N, T // cfg["patch_size"]
+    fl = dit_step_flops(cfg, Ng, S, enc_S)
+    peaks, kind = measured_peaks()
+    res = {"metric": "DiT denoise steps/s (config 4: 24 layers, hidden 2048, Q8_0, 4 tracks x CFG 2, 750 tokens, "
+                     "512 condition rows, turbo 8 Euler steps with APG)",
+           "unit": "step/s", "higher_is_better": True,
+           "config": {"workload": "config4_dit2b_q8_0_turbo8_cfg", "tracks": N, "sequences": Ng, "frames": T,
+                      "tokens": S, "enc_rows": enc_S, "steps": DIT_STEPS, "guidance": DIT_GUIDANCE,
+                      "weight_bytes_device": dit.weight_bytes(), "gguf_write_s": round(t_gen, 1)},
+           "flops_per_step": fl}
+    for mode in modes:
+        dit.set_exact(mode == "exact")
+        dit.generate(noise, ctx, enc, sched, guidance_scale=DIT_GUIDANCE)  # captures the step graphs
+        ms = []
+        import torch
+        if mode == modes[0]:
+            torch.cuda.profiler.start()  # profiler range = the first mode's timed generates
+        for _ in range(reps):
+            _, m = dit.generate(noise, ctx, enc, sched, guidance_scale=DIT_GUIDANCE)
+            ms.append(m)
+        if mode == modes[0]:
+            torch.cuda.profiler.stop()
+        step_ms = min(ms) / DIT_STEPS
+        t1 = time.perf_counter()
+        x0, _ = dit.generate(noise, ctx, enc, sched, guidance_scale=DIT_GUIDANCE)
+        e2e_s = time.perf_counter() - t1
+        res[mode] = {
+            "value": round(1e3 / step_ms, 3), "ms_per_step": round(step_ms, 3),
+            "tensor_work_multiplier": 3 if mode == "exact" else 1,
+            "roofline": {"kernel": "whole denoise step (tcgen05 GEMMs dominate)", "bound": "tensor",
+                         "achieved": round(fl / (step_ms * 1e-3) / 1e12, 1), "peak": peaks["bf16_tflops_sustained"],
+                         "peak_kind": kind + " sustained", "unit": "TFLOP/s",
+                         "frac": round(fl / (step_ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+                         "traffic": None},
+            "e2e": {"value": round(DIT_STEPS / e2e_s, 3), "unit": "step/s",
+                    "h2d_bytes_per_step": (noise.nbytes + ctx.nbytes + enc.nbytes) // DIT_STEPS,
+                    "d2h_bytes_per_step": x0.nbytes // DIT_STEPS, "path": "acb_dit_generate (host arrays)"},
+        }
+    res["value"] = res[modes[0]]["value"]
+    if want_cpu:
+        res["cpu_baseline"] = cpu_dit_sample(cfg, keep, N, T, enc_S)
+    dit.close()
+    del keep
+    try:
+        os.remove(path)
+    except OSError:
+        pass
+    return res
+
+
+def cpu_dit_sample(cfg, keep, N, T, enc_S):
+    """Oracle DiT on the host cores (bounded sample): one evaluation of the 8 CFG sequences with
+    0 and with 1 layer; a step is extrapolated as t0 + n_layers * (t1 - t0) (every layer does the
+    same work) plus the host APG/Euler (negligible)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    od = O.dit_from_gguf_tensors(cfg, keep)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((2 * N, T, cfg["in_channels"])).astype(np.float32)
+    e = rng.standard_normal((2 * N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    t0 = time.perf_counter()
+    od.forward(x, e, 0.5, 0.5, n_layers_run=0)
+    t_base = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    od.forward(x, e, 0.5, 0.5, n_layers_run=1)
+    t_one = time.perf_counter() - t0
+    step = t_base + cfg["n_layers"] * max(t_one - t_base, 0.0)
+    return {"value": round(1.0 / step, 5), "unit": "step/s", "cores": O.get_threads(), "kind": "port",
+            "sample": f"oracle evaluations of 8 sequences with 0 and 1 layers ({t_base:.1f} s, {t_one:.1f} s), "
+                      f"step extrapolated to {cfg['n_layers']} layers"}
 
 
 def cpu_lm_sample(cfg, keep, prompt, n_prefill=8, n_decode=3):
