@@ -1,8 +1,17 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 op-chain (one JSON line on rank 0).
 
-Default workload `ops` = BASELINE config 2, the isolated fused-op microbench at DiT/LM row
-shapes, in both f32 and bf16 I/O. One step runs, per I/O type:
+Headline (workload `dit`, every N): BASELINE config 4, the DiT denoiser -- 24 layers, hidden
+2048, Q8_0 weights, 4 tracks x CFG 2 = 8 sequences of 750 tokens (1500 latent frames, patch 2),
+512 condition rows, the turbo schedule with Euler steps and APG guidance. A step is one denoise
+step of the whole 8-sequence job; the sequences are sharded over the GPUs (strong scaling) and
+each step all-gathers the velocities (NCCL) before APG. The metric is denoise steps/s, in the
+exact arithmetic mode (products of the reference's dequantised operands from hi/lo f16 splits);
+the fast mode (single f16 operands) is reported beside it.
+
+Sub-results at N=1: config 1 (text encoder forwards/s), config 3 (LM decode tok/s) and config 2:
+the isolated fused-op microbench at DiT/LM row shapes, in both f32 and bf16 I/O. One step runs,
+per I/O type:
   (a) RMSNorm over 8192 rows of 2048
   (b) per-head q/k RMSNorm + NeoX RoPE on [B=4, T=1024, H=16, D=128], positions 0..T-1, theta 1e6
   (c) SwiGLU on gate/up [8192, 6144] (fused [8192, 12288] rows)
@@ -16,9 +25,8 @@ L2 across iterations.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Multi-GPU: launched under torch.distributed.run, one process per GPU; every rank runs the same
-per-GPU workload on its own rows (weak scaling, no data-path collective); timing is the max over
-ranks of the CUDA-event time.
+Multi-GPU: launched under torch.distributed.run, one process per GPU; timing is the max over ranks
+of the CUDA-event time.
 """
 from __future__ import annotations
 
@@ -250,26 +258,62 @@ def dist_env():
 
 
 def run_reference(args):
-    """Reference arm: the reference's ggml-CPU build cannot be compiled here (its ggml submodule
-    is empty), so the arm times the oracle port of its arithmetic on all host threads."""
+    """Reference arm on the headline's metric and config (config 4 DiT steps/s). The reference's
+    ggml-CPU build cannot be compiled here (its ggml submodule is empty), so the oracle port of its
+    DiT arithmetic runs on all host threads. Each timed step is a bounded sample: one evaluation
+    of a CFG pair of sequences (cond + uncond of one track) with one layer; the 0-layer cost is
+    measured once in warm-up, and a full step is (t0 + n_layers * (t1 - t0)) * 4 (every layer and
+    every sequence pair does the same work). Under torchrun only rank 0 runs."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    vals = []
-    info = {}
-    for _ in range(max(1, args.warmup // 3)):
-        cpu_ops_sample(8, os.cpu_count())
-    for _ in range(max(1, min(args.steps, 5))):
-        v, info = cpu_ops_sample(8, os.cpu_count())
-        vals.append(v)
-    val = statistics.median(vals)
-    line = {"metric": "fused-op HBM GB/s (config 2 op-chain, algorithmic bytes)", "value": round(val, 3),
-            "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": len(vals), "warmup": args.warmup,
-            "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config2_fused_ops", "io": ["f32"]},
-            "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": info["cores"], "kind": "port",
-                             "sample": info["sample"]},
-            "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import synthetic
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    O.set_threads(os.cpu_count() or 1)
+    cfg = dict(synthetic.ACESTEP_DIT_2B)
+    L = cfg["n_layers"]
+    one = dict(cfg, n_layers=1)
+    keep = {}
+    path = os.path.join(tempfile.gettempdir(), "acb_ref_dit_1layer.gguf")
+    synthetic.write_dit_gguf(path, one, synthetic.Q8_0, seed=21, device="cuda" if torch.cuda.is_available() else "cpu",
+                             keep=keep)
+    os.remove(path)
+    od = O.dit_from_gguf_tensors(one, keep)
+    rng = np.random.default_rng(1)
+    T, enc_S = DIT_T, DIT_ENC_S
+    x = rng.standard_normal((2, T, cfg["in_channels"])).astype(np.float32)
+    e = rng.standard_normal((2, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    t0 = time.perf_counter()
+    od.forward(x, e, 0.5, 0.5, n_layers_run=0)
+    t_base = time.perf_counter() - t0
+    steps = max(1, min(args.steps, 16))
+    samples = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        od.forward(x, e, 0.5, 0.5, n_layers_run=1)
+        t_one = time.perf_counter() - t0
+        samples.append((t_base + L * max(t_one - t_base, 0.0)) * (2 * DIT_TRACKS // 2))
+    step_s = statistics.median(samples)
+    val = 1.0 / step_s
+    cores = O.get_threads()
+    line = {"metric": "DiT denoise steps/s (config 4: 24 layers, hidden 2048, Q8_0, 4 tracks x CFG 2 = 8 "
+                      "sequences of 750 tokens, 512 condition rows, turbo Euler + APG)",
+            "value": round(val, 6), "unit": "step/s", "impl": "reference", "n_gpus": args.gpus, "steps": steps,
+            "warmup": 1, "ms_per_step": round(step_s * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+            "dtype": "int8 dot products (Q8_0 x Q8_0-quantised activations), f32 elsewhere", "data": "synthetic",
+            "config": {"workload": "config4_dit2b_q8_0_turbo_cfg", "tracks": DIT_TRACKS, "sequences": 2 * DIT_TRACKS,
+                       "frames": T, "enc_rows": enc_S},
+            "cpu_baseline": {"value": round(val, 6), "unit": "step/s", "cores": cores, "kind": "port",
+                             "sample": f"per step: oracle evaluation of one CFG pair (2 sequences) through 1 "
+                                       f"layer, 0-layer base {t_base:.1f} s measured once, extrapolated to {L} "
+                                       f"layers x 4 sequence pairs"},
+            "e2e": {"value": round(val, 6), "unit": "step/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "reference ggml-CPU build unavailable (ggml submodule absent); oracle port timed instead"}
     print(json.dumps(line), flush=True)
 
@@ -294,7 +338,7 @@ def run_ours(args):
     if args.workloads == "gemm":
         print(json.dumps(run_gemm_shapes(dev)), flush=True)
         return
-    if args.workloads == "dit":
+    if args.workloads == "ditmodes":
         r = run_dit(dev, rank, want_cpu=not args.no_cpu_baseline)
         if rank == 0:
             print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands (Q8_0-quantised activations)")),
@@ -313,6 +357,40 @@ def run_ours(args):
             print(json.dumps(dict(lm, n_gpus=ws, data="synthetic", dtype="int8-dot/f32")), flush=True)
         return
 
+    wl = args.workloads.split(",")
+    if "dit" not in wl:
+        # config-2 headline (legacy layout): ops line with the LM / encoder results attached
+        line = run_ops_line(args, dev, rank, ws, local, stream)
+        if "lm" in wl and ws == 1:
+            line["lm_decode"] = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt,
+                                       gen_len=args.lm_gen)
+        if "enc" in wl and ws == 1:
+            line["text_encoder"] = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
+    else:
+        line = run_dit_job(args, dev, rank, ws, local, stream)
+        if ws == 1:
+            # the other configs on one GPU, as sub-results
+            if "ops" in wl:
+                import copy
+                a2 = copy.copy(args)
+                a2.steps, a2.warmup = 300, 20
+                line["fused_ops"] = run_ops_line(a2, dev, rank, ws, local, stream)
+            if "lm" in wl:
+                torch.cuda.empty_cache()
+                line["lm_decode"] = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt,
+                                           gen_len=args.lm_gen)
+            if "enc" in wl:
+                torch.cuda.empty_cache()
+                line["text_encoder"] = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_ops_line(args, dev, rank, ws, local, stream):
+    """Config 2 (the fused-op microbench): one line dict (every rank runs a replica)."""
+    import torch
     table = make_q8_table(dev, 1234 + rank)
     wls = [OpsWorkload("f32", dev, table, 100 + rank), OpsWorkload("bf16", dev, table, 200 + rank)]
     ops = [(w.io, name, f, w.bytes[name]) for w in wls for name, f in w.ops()]
@@ -397,37 +475,25 @@ def run_ours(args):
         cpu = {"value": round(v, 3), "unit": "GB/s", "cores": info["cores"], "kind": "port",
                "sample": info["sample"]}
 
-    lm = None
-    if "lm" in args.workloads.split(",") and ws == 1:
-        del wls, ops, evs
-        torch.cuda.empty_cache()
-        lm = run_lm(dev, rank, want_cpu=not args.no_cpu_baseline, prompt_len=args.lm_prompt, gen_len=args.lm_gen)
-    enc = None
-    if "enc" in args.workloads.split(",") and ws == 1:
-        torch.cuda.empty_cache()
-        enc = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
-
-    if rank == 0:
-        line = {"metric": "fused-op HBM GB/s (config 2 op-chain, algorithmic bytes)", "value": round(value, 2),
-                "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                "config": {"workload": "config2_fused_ops", "io": ["f32", "bf16"],
-                           "ops": ["rms_norm 8192x2048", "qk_norm_rope 4x1024x16x128", "swiglu 8192x6144",
-                                   "adaln_modulate 8x750x2048", "gated_residual 8x750x2048",
-                                   "get_rows 8192 of 217472x2048 q8_0"],
-                           "bytes_per_step": step_bytes,
-                           "l2": "working set 1.7 GB per step > 126 MB L2, each buffer touched once per step",
-                           "parallelism": f"replica{ws}" if ws > 1 else "single"},
-                "roofline": roof, "per_op": {k: {"ms": round(v["ms"], 5), "GB/s": round(v["GB/s"], 1)}
-                                             for k, v in per_op.items()},
-                "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-                "gpu_launches": n_launch, "clocks": clocks, "cpu_baseline": cpu, "lm_decode": lm,
-                "text_encoder": enc}
-        print(json.dumps(line), flush=True)
-    if ws > 1:
-        torch.distributed.destroy_process_group()
+    line = {"metric": "fused-op HBM GB/s (config 2 op-chain, algorithmic bytes)", "value": round(value, 2),
+            "unit": "GB/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2_fused_ops", "io": ["f32", "bf16"],
+                       "ops": ["rms_norm 8192x2048", "qk_norm_rope 4x1024x16x128", "swiglu 8192x6144",
+                               "adaln_modulate 8x750x2048", "gated_residual 8x750x2048",
+                               "get_rows 8192 of 217472x2048 q8_0"],
+                       "bytes_per_step": step_bytes,
+                       "l2": "working set 1.7 GB per step > 126 MB L2, each buffer touched once per step",
+                       "parallelism": f"replica{ws}" if ws > 1 else "single"},
+            "roofline": roof, "per_op": {k: {"ms": round(v["ms"], 5), "GB/s": round(v["GB/s"], 1)}
+                                         for k, v in per_op.items()},
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": n_launch, "clocks": clocks, "cpu_baseline": cpu}
+    del wls, ops, evs
+    torch.cuda.empty_cache()
+    return line
 
 
 # DRAM traffic per launch from ncu captures (profiles/); None until captured.
@@ -800,27 +866,183 @@ def run_dit(dev, rank, want_cpu=True, reps=2, modes=("exact", "fast")):
     return res
 
 
+def run_dit_job(args, dev, rank, ws, local, stream):
+    """The headline: config 4 denoise steps/s for the whole 8-sequence job (4 tracks x CFG 2), the
+    sequences sharded over the ranks (strong scaling). Each step: every rank evaluates its own
+    sequences (acb_dit_eval, one CUDA graph); an NCCL all-gather assembles the velocities; every
+    rank runs APG + the Euler update for all tracks (identical on every rank). A step of the
+    turbo schedule is one timed unit; after the 8th step the next generation starts from the
+    noise again."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+    import synthetic
+
+    cfg = dict(synthetic.ACESTEP_DIT_2B)
+    N, T, enc_S, Oc = DIT_TRACKS, DIT_T, DIT_ENC_S, cfg["out_channels"]
+    Ng, S, ctx_ch = 2 * N, T // cfg["patch_size"], cfg["in_channels"] - Oc
+    if Ng % ws != 0:
+        raise SystemExit(f"the {Ng} sequences of config 4 do not shard over {ws} GPUs")
+    n_loc = Ng // ws
+    slots = list(range(rank * n_loc, (rank + 1) * n_loc))
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    # one synthetic checkpoint for all ranks: rank 0 writes it, everyone loads it
+    path = os.path.join(tempfile.gettempdir(), "acb_bench_dit2b_q8_0.gguf")
+    keep = {} if (rank == 0 and ws == 1 and not args.no_cpu_baseline) else None
+    if rank == 0:
+        synthetic.write_dit_gguf(path, cfg, synthetic.Q8_0, seed=21, device=str(dev), keep=keep)
+    barrier()
+    dit = acb.DiT(path, device=local)
+    import gguf
+    null = np.array([t for t in gguf.GGUFReader(path).tensors if t.name == "null_condition_emb"][0].data,
+                    dtype=np.float32).reshape(-1)
+    barrier()
+    if rank == 0:
+        os.remove(path)
+
+    rng = np.random.default_rng(17)
+    noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((N, T, ctx_ch)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    enc_loc = np.stack([enc[j] if j < N else np.broadcast_to(null, enc.shape[1:]) for j in slots])
+    dit.set_condition(torch.from_numpy(np.ascontiguousarray(enc_loc)).to(dev), T)
+    tracks = torch.tensor([j % N for j in slots], device=dev)
+    inp = torch.zeros((n_loc, T, cfg["in_channels"]), device=dev)
+    inp[:, :, :ctx_ch] = torch.from_numpy(ctx).to(dev)[tracks]
+    noise_d = torch.from_numpy(noise).to(dev)
+    xt = noise_d.clone()
+    vel_loc = torch.empty((n_loc, T, Oc), device=dev)
+    vel_all = torch.empty((Ng, T, Oc), device=dev) if ws > 1 else vel_loc
+    vt = torch.empty((N, T, Oc), device=dev)
+    x0 = torch.empty((N, T, Oc), device=dev)
+    ra = torch.empty((N, T, Oc), dtype=torch.float64, device=dev)
+    sched = acb.turbo_schedule(DIT_STEPS)
+    tts = torch.tensor([[t, t, sched[i + 1] if i + 1 < DIT_STEPS else 0.0] for i, t in enumerate(sched)],
+                       dtype=torch.float32, device=dev)
+
+    def step(k, h_tt=None, h_out=None):
+        i = k % DIT_STEPS
+        tt = tts[i]
+        if h_tt is not None:  # end-to-end: this step's timestep row from pinned host memory
+            tt = h_tt[1]
+            tt.copy_(h_tt[0][i], non_blocking=True)
+        inp[:, :, ctx_ch:] = xt[tracks]
+        dit.eval(inp, tt, vel_loc)
+        if ws > 1:
+            torch.distributed.all_gather_into_tensor(vel_all, vel_loc)
+        acb.dit_apg(vel_all[:N], vel_all[N:], ra, i == 0, DIT_GUIDANCE, vt)
+        last = i == DIT_STEPS - 1
+        acb.dit_euler(xt, vt, tt, last, out=x0)
+        if last:
+            xt.copy_(noise_d)
+        if h_out is not None:  # end-to-end: the step's result back to pinned host memory
+            h_out.copy_(x0 if last else xt, non_blocking=True)
+
+    def timed(K, **kw):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(K):
+            step(k, **kw)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if ws > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    peaks, kind = measured_peaks()
+    fl = dit_step_flops(cfg, Ng, S, enc_S)
+    out = {}
+    for mode in ("fast", "exact"):  # the headline mode last, so its graphs are the live ones
+        dit.set_exact(mode == "exact")
+        for k in range(max(args.warmup, 3)):
+            step(k)
+        K = args.steps if mode == "exact" else min(args.steps, DIT_STEPS)
+        clk = ClockSampler(local) if mode == "exact" else None
+        if clk:
+            clk.start()
+            time.sleep(0.3)
+        ms = timed(K)
+        clocks = clk.stop() if clk else None
+        step_ms = ms / K
+        out[mode] = {"value": round(K / (ms * 1e-3), 3), "ms_per_step": round(step_ms, 3), "steps": K,
+                     "clocks": clocks,
+                     "roofline": {"kernel": "whole denoise step (tcgen05 GEMMs dominate)", "bound": "tensor",
+                                  "achieved": round(fl / ws / (step_ms * 1e-3) / 1e12, 1),
+                                  "peak": peaks["bf16_tflops_sustained"], "peak_kind": kind + " sustained",
+                                  "unit": "TFLOP/s",
+                                  "frac": round(fl / ws / (step_ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
+                                  "traffic": None, "tensor_work_multiplier": 3 if mode == "exact" else 1}}
+    # end to end: the same steps with the timestep row copied in from pinned host memory and the
+    # step's result (xt, or x0 at the last step) read back to pinned host memory every step
+    h_tts = torch.empty((DIT_STEPS, 3), dtype=torch.float32, pin_memory=True).copy_(tts)
+    d_tt = torch.empty(3, dtype=torch.float32, device=dev)
+    h_out = torch.empty((N, T, Oc), dtype=torch.float32, pin_memory=True)
+    e2e_k = DIT_STEPS
+    e2e_ms = timed(e2e_k, h_tt=(h_tts, d_tt), h_out=h_out)
+    ex = out["exact"]
+    launches = dit.eval_kernels() + 2  # evaluation graph + APG + Euler per step
+    line = {"metric": "DiT denoise steps/s (config 4: 24 layers, hidden 2048, Q8_0, 4 tracks x CFG 2 = 8 "
+                      "sequences of 750 tokens, 512 condition rows, turbo Euler + APG)",
+            "value": ex["value"], "unit": "step/s", "n_gpus": ws, "steps": ex["steps"], "warmup": max(args.warmup, 3),
+            "ms_per_step": ex["ms_per_step"], "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 hi/lo split operands (exact products of Q8_0 weights and Q8_0-quantised activations), "
+                     "fp32 accumulation",
+            "data": "synthetic (random N(0,0.02) weights in Q8_0, N(0,1) latents and condition, seeded)",
+            "config": {"workload": "config4_dit2b_q8_0_turbo_cfg", "tracks": N, "sequences": Ng,
+                       "sequences_per_gpu": n_loc, "frames": T, "tokens": S, "enc_rows": enc_S,
+                       "schedule": "turbo shift 3, 8 steps (cycled)", "guidance": DIT_GUIDANCE,
+                       "parallelism": f"sequence-sharded dp{ws}, NCCL all-gather of velocities per step"
+                                      if ws > 1 else "single",
+                       "l2": "weights 9.4 GB and activations > 126 MB L2: every step streams from HBM",
+                       "flops_per_step": fl},
+            "roofline": ex["roofline"], "clocks": ex["clocks"],
+            "e2e": {"value": round(e2e_k / (e2e_ms * 1e-3), 3), "unit": "step/s", "h2d_bytes_per_step": 12,
+                    "d2h_bytes_per_step": N * T * Oc * 4,
+                    "path": "acb_dit_eval + acb_dit_apg + acb_dit_euler with per-step pinned host copies"},
+            "gpu_launches": launches * ex["steps"],
+            "fast_mode": {k: out["fast"][k] for k in ("value", "ms_per_step", "roofline")}}
+    if keep is not None:
+        line["cpu_baseline"] = cpu_dit_sample(cfg, keep, N, T, enc_S)
+    dit.close()
+    del keep
+    torch.cuda.empty_cache()
+    return line
+
+
 def cpu_dit_sample(cfg, keep, N, T, enc_S):
-    """Oracle DiT on the host cores (bounded sample): one evaluation of the 8 CFG sequences with
-    0 and with 1 layer; a step is extrapolated as t0 + n_layers * (t1 - t0) (every layer does the
-    same work) plus the host APG/Euler (negligible)."""
+    """Oracle DiT on the host cores (bounded sample, the reference arm's method): one CFG pair of
+    sequences evaluated with 0 and with 1 layer; a step of the 2N-sequence job is
+    (t0 + n_layers * (t1 - t0)) * N (every layer and every pair does the same work)."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     od = O.dit_from_gguf_tensors(cfg, keep)
     rng = np.random.default_rng(1)
-    x = rng.standard_normal((2 * N, T, cfg["in_channels"])).astype(np.float32)
-    e = rng.standard_normal((2 * N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    x = rng.standard_normal((2, T, cfg["in_channels"])).astype(np.float32)
+    e = rng.standard_normal((2, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
     t0 = time.perf_counter()
     od.forward(x, e, 0.5, 0.5, n_layers_run=0)
     t_base = time.perf_counter() - t0
     t0 = time.perf_counter()
     od.forward(x, e, 0.5, 0.5, n_layers_run=1)
     t_one = time.perf_counter() - t0
-    step = t_base + cfg["n_layers"] * max(t_one - t_base, 0.0)
-    return {"value": round(1.0 / step, 5), "unit": "step/s", "cores": O.get_threads(), "kind": "port",
-            "sample": f"oracle evaluations of 8 sequences with 0 and 1 layers ({t_base:.1f} s, {t_one:.1f} s), "
-                      f"step extrapolated to {cfg['n_layers']} layers"}
+    step = (t_base + cfg["n_layers"] * max(t_one - t_base, 0.0)) * N
+    return {"value": round(1.0 / step, 6), "unit": "step/s", "cores": O.get_threads(), "kind": "port",
+            "sample": f"oracle evaluations of one CFG pair with 0 and 1 layers ({t_base:.1f} s, {t_one:.1f} s), "
+                      f"extrapolated to {cfg['n_layers']} layers x {N} pairs"}
 
 
 def cpu_lm_sample(cfg, keep, prompt, n_prefill=8, n_decode=3):
@@ -849,15 +1071,16 @@ def cpu_lm_sample(cfg, keep, prompt, n_prefill=8, n_decode=3):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=16, help="timed DiT denoise steps (the headline unit)")
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
-    ap.add_argument("--workloads", default="ops,lm,enc",
-                    help="comma list: ops (config 2, the headline line), lm (config 3 decode, N=1), "
-                         "enc (config 1 text encoder, N=1); or `gemv` / `gemm` / `enc` alone")
+    ap.add_argument("--workloads", default="dit,ops,lm,enc",
+                    help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
+                         "decode), enc (config 1 text encoder) -- the last three at N=1 as sub-results; without "
+                         "dit, ops is the headline; or one of gemv / gemm / enc / ditmodes alone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -106,6 +106,11 @@ def lib():
             "acb_dit_forward": (I, [P, P, P, I, I, I, F, F, P, I, P]),
             "acb_dit_generate": (I, [P, P, P, P, I, I, I, I, P, P, F, P]),
             "acb_dit_free": (None, [P]),
+            "acb_dit_set_condition": (I, [P, P, I, I, I, P]),
+            "acb_dit_eval_kernels": (I, [P]),
+            "acb_dit_eval": (I, [P, P, P, P, P]),
+            "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
+            "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
             "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_attn_prefill_split": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I,
                                            I, I, F, I, I64, I64, I64, P]),
@@ -601,6 +606,16 @@ class DiT:
                                                         float(t_r), _ptr(out), n_layers_run, _stream(stream)))
         return out
 
+    def set_condition(self, enc, T, stream=None):
+        """enc [N, enc_S, enc_hidden] f32 CUDA tensor: embed it and cache the cross K/V."""
+        _check("acb_dit_set_condition", lib().acb_dit_set_condition(self.h, _ptr(enc), enc.shape[0], T, enc.shape[1],
+                                                                    _stream(stream)))
+
+    def eval(self, x, tt, out, stream=None):
+        """One evaluation of x [N, T, in_channels] with tt = device tensor [t, t_r] into out."""
+        _check("acb_dit_eval", lib().acb_dit_eval(self.h, _ptr(x), _ptr(tt), _ptr(out), _stream(stream)))
+        return out
+
     def generate(self, noise, context, enc, schedule, guidance_scale=1.0):
         """Host arrays: noise [N, T, Oc], context [N, T, in-Oc], enc [N, enc_S, enc_hidden] ->
         (x0 [N, T, Oc], device ms of the step loop)."""
@@ -626,4 +641,19 @@ def turbo_schedule(steps=8, shift=3.0):
     for i in range(steps):
         t = f(1.0) - f(i) / f(steps)  # float arithmetic as in the reference
         out.append(float(f(shift) * t / (f(1.0) + (f(shift) - f(1.0)) * t)))
+    return out
+
+
+def dit_apg(cond, uncond, running_avg, first, guidance_scale, out, momentum=-0.75, norm_threshold=2.5, stream=None):
+    """APG over cond/uncond [N, T, Oc] CUDA f32 (running_avg float64 [N, T, Oc]) into out."""
+    N, T, Oc = cond.shape
+    _check("acb_dit_apg", lib().acb_dit_apg(_ptr(cond), _ptr(uncond), _ptr(running_avg), int(first), momentum,
+                                            guidance_scale, norm_threshold, N, T, Oc, _ptr(out), _stream(stream)))
+    return out
+
+
+def dit_euler(xt, vt, tt3, last, out=None, stream=None):
+    """tt3 = device [t_curr, t_r, t_next]: xt -= vt * (t_curr - t_next), or out = xt - vt * t_curr."""
+    _check("acb_dit_euler", lib().acb_dit_euler(_ptr(xt), _ptr(vt), _ptr(tt3), int(last), _ptr(out), xt.numel(),
+                                                _stream(stream)))
     return out

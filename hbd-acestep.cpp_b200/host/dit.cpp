@@ -72,6 +72,7 @@ struct acb_dit {
     DevBuf input, h, xn, xq, qkv32, qkv16, planes, q16, k16, att, gu, vel, pos, rope, ws, err;
     DevBuf enc_in, enc_h, kv32, kvcache;  // condition: raw [Ng][enc_S][H_enc], embedded, per-layer K/V planes
     size_t kv_layer_elems = 0;            // elements of one plane of one layer's cached K||V
+    int    eval_kernels   = 0;            // kernel launches of one captured evaluation
     // generate
     DevBuf                          xt, vt, out, ra;
     std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
@@ -671,6 +672,72 @@ extern "C" acb_status acb_dit_forward(acb_dit * m, const float * d_input, const 
     return cudaStreamSynchronize(s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
 }
 
+extern "C" acb_status acb_dit_set_condition(acb_dit * m, const float * d_enc, int N, int T, int enc_S,
+                                            acb_stream_t stream) {
+    if (!m || !d_enc || N <= 0 || T <= 0 || enc_S <= 0 || T % m->c.patch_size != 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    ACB_TRY(m->reserve(N, T, enc_S));
+    cudaStream_t s   = (cudaStream_t) stream;
+    const size_t nen = (size_t) N * enc_S * m->c.enc_hidden_size * 4;
+    if (cudaMemcpyAsync(m->enc_in.p, d_enc, nen, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    return m->condition(s);
+}
+
+extern "C" acb_status acb_dit_eval(acb_dit * m, const float * d_input, const float * tt, float * d_velocity,
+                                   acb_stream_t stream) {
+    if (!m || !d_input || !tt || !d_velocity || m->Ng <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    cudaStream_t  s   = (cudaStream_t) stream;
+    const int     T   = m->S * m->c.patch_size;
+    const size_t  nin = (size_t) m->Ng * T * m->c.in_channels * 4;
+    const size_t  nv  = (size_t) m->Ng * T * m->c.out_channels * 4;
+    // the evaluation chain for this shape is one graph over the model's buffers
+    const auto key = std::make_tuple(m->Ng * 100000 + T, m->enc_S, 2, 0, m->exact ? 1 : 0, 0u);
+    auto       it  = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        const acb_status  es = m->evaluate(-1, m->st);
+        const cudaError_t ce = cudaStreamEndCapture(m->st, &g);
+        if (es != ACB_OK || ce != cudaSuccess) {
+            if (g) {
+                cudaGraphDestroy(g);
+            }
+            set_last_error("DiT evaluation graph capture failed");
+            return es != ACB_OK ? es : ACB_ERR_CUDA;
+        }
+        size_t n_nodes = 0;  // every node of the evaluation graph is one of this library's kernels
+        cudaGraphGetNodes(g, nullptr, &n_nodes);
+        m->eval_kernels      = (int) n_nodes;
+        cudaGraphExec_t   ex = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        it = m->graphs.emplace(key, ex).first;
+    }
+    if (cudaMemcpyAsync(m->tt.p, tt, 2 * sizeof(float), cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(m->input.p, d_input, nin, cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+        cudaGraphLaunch(it->second, s) != cudaSuccess ||
+        cudaMemcpyAsync(d_velocity, m->vel.p, nv, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
 extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
                                        const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                        const float * schedule, float * output, float guidance_scale, float * gpu_ms) {
@@ -824,6 +891,10 @@ extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const f
         return ACB_ERR_DEVICE;
     }
     return st;
+}
+
+extern "C" int acb_dit_eval_kernels(const acb_dit * m) {
+    return m ? m->eval_kernels : 0;
 }
 
 extern "C" void acb_dit_free(acb_dit * m) {

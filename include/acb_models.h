@@ -130,6 +130,18 @@ ACB_API acb_status acb_dit_set_exact(acb_dit * m, int exact);
 ACB_API acb_status acb_dit_forward(acb_dit * m, const float * d_input, const float * d_enc, int N, int T, int enc_S,
                                    float t, float t_r, float * d_velocity, int n_layers_run, acb_stream_t stream);
 
+/* The two halves of acb_dit_forward for callers that run their own step loop (e.g. sequences
+ * sharded over GPUs): set_condition embeds enc [N][enc_S][enc_hidden_size] (device) and caches
+ * every layer's cross-attention K/V for N sequences of T frames; eval runs one evaluation of
+ * input [N][T][in_channels] (device) with tt = {t, t_r} (device floats) into velocity, as one
+ * CUDA graph per shape (captured on first use), enqueued on `stream` without synchronising. */
+ACB_API acb_status acb_dit_set_condition(acb_dit * m, const float * d_enc, int N, int T, int enc_S,
+                                         acb_stream_t stream);
+ACB_API acb_status acb_dit_eval(acb_dit * m, const float * d_input, const float * tt, float * d_velocity,
+                                acb_stream_t stream);
+/* Kernel launches in the last captured evaluation graph (0 before the first acb_dit_eval). */
+ACB_API int        acb_dit_eval_kernels(const acb_dit * m);
+
 /* dit_ggml_generate (dit-sampler.h:132-711) with the Euler solver, host arrays as in the reference:
  * noise [N][T][out_channels], context_latents [N][T][in_channels - out_channels], enc_hidden
  * [N][enc_S][enc_hidden_size], schedule[num_steps] -> output [N][T][out_channels] (the x0
