@@ -606,6 +606,10 @@ class DiT:
                                                         float(t_r), _ptr(out), n_layers_run, _stream(stream)))
         return out
 
+    def eval_kernels(self) -> int:
+        """Kernel launches in the last captured evaluation graph."""
+        return lib().acb_dit_eval_kernels(self.h)
+
     def set_condition(self, enc, T, stream=None):
         """enc [N, enc_S, enc_hidden] f32 CUDA tensor: embed it and cache the cross K/V."""
         _check("acb_dit_set_condition", lib().acb_dit_set_condition(self.h, _ptr(enc), enc.shape[0], T, enc.shape[1],
