@@ -335,8 +335,13 @@ def run_ours(args):
     if args.workloads == "gemv":
         print(json.dumps(run_gemv_shapes(dev)), flush=True)
         return
-    if args.workloads == "gemm":
-        print(json.dumps(run_gemm_shapes(dev)), flush=True)
+    if args.workloads.startswith("gemm"):
+        which = args.workloads.split(":")[1].split("+") if ":" in args.workloads else None
+        print(json.dumps(run_gemm_shapes(dev, which=which)), flush=True)
+        return
+    if args.workloads.startswith("attn"):
+        which = args.workloads.split(":")[1].split("+") if ":" in args.workloads else None
+        print(json.dumps(run_attn_shapes(dev, which=which)), flush=True)
         return
     if args.workloads == "ditmodes":
         r = run_dit(dev, rank, want_cpu=not args.no_cpu_baseline)
@@ -541,31 +546,87 @@ GEMM_SHAPES = [("sa_qkv", 6000, 4096, 2048), ("sa_o", 6000, 2048, 2048), ("gate_
                ("down", 6000, 2048, 6144)]
 
 
-def run_gemm_shapes(dev, reps=20):
-    """acb_gemm_bf16 (bf16 in, f32 accumulate, bf16 out) per DiT linear shape, CUDA events around
-    `reps` launches after 3 warm-ups; TFLOP/s against the measured bf16 peak."""
+def run_gemm_shapes(dev, reps=20, which=None):
+    """acb_gemm_tc per DiT linear shape, CUDA events around `reps` launches after 3 warm-ups:
+    bf16 operands over K, and the exact mode's f16 operands over K' = 3K (hi/lo splits). TFLOP/s
+    of tensor work against the measured bf16 peak."""
     import torch
 
     import acb
     peaks, kind = measured_peaks()
-    out = {"metric": "tcgen05 bf16 GEMM TFLOP/s per DiT shape", "peak_tflops": peaks["bf16_tflops"],
+    out = {"metric": "tcgen05 GEMM TFLOP/s per DiT shape (tensor work)", "peak_tflops": peaks["bf16_tflops"],
            "peak_kind": kind, "shapes": {}}
     for name, M, N, K in GEMM_SHAPES:
-        A = torch.randn(M, K, device=dev).bfloat16()
-        B = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
-        C = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-        for _ in range(3):
-            acb.gemm_bf16(A, B, out=C)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            acb.gemm_bf16(A, B, out=C)
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) / reps * 1e3
-        tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
-        out["shapes"][name] = {"M": M, "N": N, "K": K, "us": round(us, 1), "TFLOP/s": round(tf, 1),
-                               "frac": round(tf / peaks["bf16_tflops"], 3)}
+        if which and name not in which:
+            continue
+        res = {"M": M, "N": N, "K": K}
+        for mode, dt, Kp in (("bf16", torch.bfloat16, K), ("f16_exact3K", torch.float16, 3 * K)):
+            A = torch.randn(M, Kp, device=dev).to(dt)
+            B = (torch.randn(N, Kp, device=dev) * 0.02).to(dt)
+            C = torch.empty(M, N, device=dev, dtype=torch.float32)
+            for _ in range(3):
+                acb.gemm_bf16(A, B, out=C)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                acb.gemm_bf16(A, B, out=C)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            tf = 2.0 * M * N * Kp / (us * 1e-6) / 1e12
+            res[mode] = {"us": round(us, 1), "TFLOP/s": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 3)}
+            del A, B, C
+        out["shapes"][name] = res
+    return out
+
+
+ATTN_SHAPES = [("dit_self_window", 8, 750, 750, 2, 128), ("dit_self_full", 8, 750, 750, 0, 0),
+               ("dit_cross", 8, 750, 512, 0, 0), ("enc_causal", 1, 256, 256, 1, 0)]
+
+
+def run_attn_shapes(dev, reps=10, which=None):
+    """acb_attn_prefill (f16 operands) and acb_attn_prefill_split (hi/lo planes, the exact mode)
+    per attention shape of configs 1 and 4 (16 q heads, 8 kv heads, D 128), CUDA events around
+    `reps` launches after 3 warm-ups; algorithmic TFLOP/s (QK^T and PV over the unmasked pairs)."""
+    import torch
+
+    import acb
+    out = {"metric": "prefill/DiT attention algorithmic TFLOP/s per shape", "shapes": {}}
+    Nh, Nkv, D = 16, 8, 128
+    for name, B, Sq, Skv, mask, win in ATTN_SHAPES:
+        if which and name not in which:
+            continue
+        g = torch.Generator(device=dev).manual_seed(Sq + Skv)
+        q = torch.randn(B, Sq, Nh * D, device=dev, generator=g)
+        k = torch.randn(B, Skv, Nkv * D, device=dev, generator=g)
+        v = torch.randn(B, Skv, Nkv * D, device=dev, generator=g)
+        planes = [acb.act_quant_ex(t.reshape(-1, t.shape[-1]), t.shape[-1], acb.F16, acb.LAYOUT_PLANES)
+                  for t in (q, k, v)]
+        hi = [p[: p.shape[0] // 2].view(t.shape) for p, t in zip(planes, (q, k, v))]
+        lo = [t.numel() for t in (q, k, v)]
+        o = torch.empty(B, Sq, Nh * D, device=dev)
+        pairs = sum(min(Skv, i + win + 1) - max(0, i - win) for i in range(Sq)) if mask == 2 else \
+            (Sq * (Sq + 1) // 2 if mask == 1 else Sq * Skv)
+        fl = 4.0 * D * Nh * B * pairs
+        res = {"B": B, "Sq": Sq, "Skv": Skv, "mask": mask}
+        for mode in ("f16", "split"):
+            def call():
+                if mode == "f16":
+                    acb.attn_prefill(hi[0], hi[1], hi[2], Nh, Nkv, mask=mask, window=win, out=o)
+                else:
+                    acb.attn_prefill_split(hi[0], hi[1], hi[2], lo[0], lo[1], lo[2], Nh, Nkv, mask=mask,
+                                           window=win, out=o)
+            for _ in range(3):
+                call()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                call()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            res[mode] = {"us": round(us, 1), "TFLOP/s": round(fl / (us * 1e-6) / 1e12, 1)}
+        out["shapes"][name] = res
     return out
 
 
