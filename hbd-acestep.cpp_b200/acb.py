@@ -107,6 +107,9 @@ def lib():
             "acb_dit_generate": (I, [P, P, P, P, I, I, I, I, P, P, F, P]),
             "acb_dit_free": (None, [P]),
             "acb_dit_set_condition": (I, [P, P, I, I, I, P]),
+            "acb_attn_tc": (I, [P, I64, P, I64, P, I64, P, I, I64, I, I, I, I, I, I, I, I, I, F, I, I64, I64, I64, P,
+                                P]),
+            "acb_attn_vt": (I, [P, I, I64, I64, I, I, I, I, P, I64, I64, P]),
             "acb_dit_eval_kernels": (I, [P]),
             "acb_dit_eval": (I, [P, P, P, P, P]),
             "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
@@ -660,4 +663,33 @@ def dit_euler(xt, vt, tt3, last, out=None, stream=None):
     """tt3 = device [t_curr, t_r, t_next]: xt -= vt * (t_curr - t_next), or out = xt - vt * t_curr."""
     _check("acb_dit_euler", lib().acb_dit_euler(_ptr(xt), _ptr(vt), _ptr(tt3), int(last), _ptr(out), xt.numel(),
                                                 _stream(stream)))
+    return out
+
+
+def attn_vt(v, Nkv, lo=False, vt_ld=None, out=None, stream=None):
+    """v [B, S, >=Nkv*128] (f32 or f16 view) -> V^T f16 [B, Nkv, 128, vt_ld] (and its lo plane:
+    returns (vt, lo_offset))."""
+    import torch
+    B, S = v.shape[0], v.shape[1]
+    ld = vt_ld or ((S + 7) // 8 * 8)
+    n = B * Nkv * 128 * ld
+    if out is None:
+        out = torch.zeros((2 if lo else 1) * n, dtype=torch.float16, device=v.device)
+    _check("acb_attn_vt", lib().acb_attn_vt(_ptr(v), dtype_id(v), v.stride(0), v.stride(1), B, S, Nkv, 128, _ptr(out),
+                                            ld, n if lo else 0, _stream(stream)))
+    return out, ld, (n if lo else 0)
+
+
+def attn_tc(q, k, vt, vt_ld, Nh, Nkv, Sq, Skv, batch, mask=MASK_NONE, window=0, causal_off=0, out=None,
+            out_dtype=None, scale=None, q_lo=0, k_lo=0, vt_lo=0, flags=0, err=None, stream=None):
+    """q [batch*Sq, q_ts], k [batch*Skv, k_ts] f16 (views allowed), vt from attn_vt -> o [batch*Sq, Nh*128]."""
+    import math
+
+    import torch
+    if out is None:
+        out = torch.empty((batch * Sq, Nh * 128), dtype=out_dtype or torch.float32, device=q.device)
+    _check("acb_attn_tc", lib().acb_attn_tc(
+        _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(vt), vt_ld, _ptr(out), dtype_id(out), out.stride(0), batch,
+        Sq, Skv, Nh, Nkv, 128, mask, window, causal_off, scale if scale is not None else 1.0 / math.sqrt(128), flags,
+        q_lo, k_lo, vt_lo, _ptr(err), _stream(stream)))
     return out

@@ -3,7 +3,7 @@
 // cross-attention to the condition; src/dit-graph.h:218-231, 339-352):
 //     O[b,i,h,:] = softmax_j( Q[b,i,h,:] . K[b,j,h/G,:] * scale + mask(i,j) ) V[b,j,h/G,:]
 // Flash-attention tiling with bf16 or f16 tensor-core MMAs (mma.sync m16n8k16, fp32 accumulation):
-// a CTA owns 64 queries of one (batch, head); four warps own 16 query rows each with their Q
+// a CTA owns 128 queries of one (batch, head); eight warps own 16 query rows each with their Q
 // fragments in registers; 64-key K/V blocks stream through a cp.async double buffer (rows padded
 // to 272 bytes so ldmatrix is conflict-free); the softmax is online in fp32 (exp2 with the scale
 // folded into log2 e); blocks wholly outside a causal or sliding-window mask are skipped.
@@ -13,10 +13,10 @@
 namespace acb {
 
 constexpr int kAttnD    = 128;
-constexpr int kAttnBQ   = 64;
+constexpr int kAttnBQ   = 128;  // queries per CTA: 8 warps of 16 rows
 constexpr int kAttnBK   = 64;
 constexpr int kAttnPad  = kAttnD + 8;  // bf16 elements per smem row
-constexpr int kAttnThreads = 128;
+constexpr int kAttnThreads = kAttnBQ * 2;
 
 enum { MASK_NONE = 0, MASK_CAUSAL = 1, MASK_WINDOW = 2 };
 
@@ -90,10 +90,11 @@ template <bool F16> __device__ __forceinline__ uint32_t pack16(float lo, float h
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// load a [64][128] bf16 tile (rows row0.., clipped to nrows) into padded smem
+// load a [ROWS][128] 16-bit tile (rows row0.., clipped to nrows) into padded smem
+template <int ROWS>
 __device__ __forceinline__ void load_tile(__nv_bfloat16 * sm, const __nv_bfloat16 * g, int64_t ts, int row0,
                                           int nrows) {
-    for (int c = threadIdx.x; c < 64 * 16; c += kAttnThreads) {
+    for (int c = threadIdx.x; c < ROWS * 16; c += kAttnThreads) {
         const int  r  = c >> 4, col = (c & 15) * 8;
         const bool ok = row0 + r < nrows;
         cp_async16(sm + r * kAttnPad + col, g + (int64_t) (ok ? row0 + r : 0) * ts + col, ok);
@@ -106,13 +107,14 @@ __device__ __forceinline__ void load_tile(__nv_bfloat16 * sm, const __nv_bfloat1
 template <int MASK, bool F16, bool SPLIT>
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    constexpr int   kTile = kAttnBQ * kAttnPad;        // elements per padded 64-row tile
+    constexpr int   kQTile = kAttnBQ * kAttnPad;       // elements of the padded query tile
+    constexpr int   kKTile = kAttnBK * kAttnPad;       // elements of one padded key/value tile
     __nv_bfloat16 * sQ = reinterpret_cast<__nv_bfloat16 *>(smem_raw);
-    __nv_bfloat16 * sK = sQ + kTile;                   // 2 buffers
-    __nv_bfloat16 * sV = sK + 2 * kTile;               // 2 buffers
-    __nv_bfloat16 * sQl = sV + 2 * kTile;              // SPLIT only: lo planes
-    __nv_bfloat16 * sKl = sQl + kTile;
-    __nv_bfloat16 * sVl = sKl + 2 * kTile;
+    __nv_bfloat16 * sK = sQ + kQTile;                  // 2 buffers
+    __nv_bfloat16 * sV = sK + 2 * kKTile;              // 2 buffers
+    __nv_bfloat16 * sQl = sV + 2 * kKTile;             // SPLIT only: lo planes
+    __nv_bfloat16 * sKl = sQl + kQTile;
+    __nv_bfloat16 * sVl = sKl + 2 * kKTile;
 
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,16 +136,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
         kb_hi = min(kb_hi, (min(q0 + kAttnBQ, a.Sq) - 1 + a.window) / kAttnBK + 1);
     }
 
-    load_tile(sQ, Qg + (int64_t) 0, a.q_ts, q0, a.Sq);
+    load_tile<kAttnBQ>(sQ, Qg + (int64_t) 0, a.q_ts, q0, a.Sq);
     if (SPLIT) {
-        load_tile(sQl, Qg + a.q_lo, a.q_ts, q0, a.Sq);
+        load_tile<kAttnBQ>(sQl, Qg + a.q_lo, a.q_ts, q0, a.Sq);
     }
     if (kb_lo < kb_hi) {
-        load_tile(sK, Kg, a.k_ts, kb_lo * kAttnBK, a.Skv);
-        load_tile(sV, Vg, a.v_ts, kb_lo * kAttnBK, a.Skv);
+        load_tile<kAttnBK>(sK, Kg, a.k_ts, kb_lo * kAttnBK, a.Skv);
+        load_tile<kAttnBK>(sV, Vg, a.v_ts, kb_lo * kAttnBK, a.Skv);
         if (SPLIT) {
-            load_tile(sKl, Kg + a.k_lo, a.k_ts, kb_lo * kAttnBK, a.Skv);
-            load_tile(sVl, Vg + a.v_lo, a.v_ts, kb_lo * kAttnBK, a.Skv);
+            load_tile<kAttnBK>(sKl, Kg + a.k_lo, a.k_ts, kb_lo * kAttnBK, a.Skv);
+            load_tile<kAttnBK>(sVl, Vg + a.v_lo, a.v_ts, kb_lo * kAttnBK, a.Skv);
         }
     }
     cp_async_commit();
@@ -163,11 +165,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const AttnAr
     for (int kb = kb_lo; kb < kb_hi; kb++) {
         const int buf = (kb - kb_lo) & 1;
         if (kb + 1 < kb_hi) {
-            load_tile(sK + (buf ^ 1) * kAttnBK * kAttnPad, Kg, a.k_ts, (kb + 1) * kAttnBK, a.Skv);
-            load_tile(sV + (buf ^ 1) * kAttnBK * kAttnPad, Vg, a.v_ts, (kb + 1) * kAttnBK, a.Skv);
+            load_tile<kAttnBK>(sK + (buf ^ 1) * kKTile, Kg, a.k_ts, (kb + 1) * kAttnBK, a.Skv);
+            load_tile<kAttnBK>(sV + (buf ^ 1) * kKTile, Vg, a.v_ts, (kb + 1) * kAttnBK, a.Skv);
             if (SPLIT) {
-                load_tile(sKl + (buf ^ 1) * kAttnBK * kAttnPad, Kg + a.k_lo, a.k_ts, (kb + 1) * kAttnBK, a.Skv);
-                load_tile(sVl + (buf ^ 1) * kAttnBK * kAttnPad, Vg + a.v_lo, a.v_ts, (kb + 1) * kAttnBK, a.Skv);
+                load_tile<kAttnBK>(sKl + (buf ^ 1) * kKTile, Kg + a.k_lo, a.k_ts, (kb + 1) * kAttnBK, a.Skv);
+                load_tile<kAttnBK>(sVl + (buf ^ 1) * kKTile, Vg + a.v_lo, a.v_ts, (kb + 1) * kAttnBK, a.Skv);
             }
         }
         cp_async_commit();
@@ -395,7 +397,7 @@ static acb_status attn_launch(const void * q, int64_t q_bs, int64_t q_ts, const 
     a.q_lo       = q_lo;
     a.k_lo       = k_lo;
     a.v_lo       = v_lo;
-    const size_t smem = (size_t) (split ? 10 : 5) * kAttnBQ * kAttnPad * 2;
+    const size_t smem = (size_t) ((split ? 2 : 1) * kAttnBQ + (split ? 8 : 4) * kAttnBK) * kAttnPad * 2;
     const dim3   grid((unsigned) ((Sq + kAttnBQ - 1) / kAttnBQ), (unsigned) Nh, (unsigned) batch);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim            = grid;

@@ -1,0 +1,508 @@
+// k_attn_tc.cu -- attention over whole sequences on the 5th-generation tensor cores, for the text
+// encoder (src/qwen3-enc.h:186-199) and the DiT (src/dit-graph.h:218-231 self-attention with the
+// sliding window of the even layers, 339-352 cross-attention):
+//     O[b,i,h,:] = softmax_j( Q[b,i,h,:] . K[b,j,h/G,:] * scale + mask(i,j) ) V[b,j,h/G,:]
+//
+// One CTA per (128 queries, head, batch), 6 warps:
+//   warp 0      TMA: the Q tile once, then key blocks of 64 (K [64][128] and V^T [128][64]) into a
+//               2-3 stage ring, all 128-byte swizzled K-major tiles;
+//   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma: S = Q.K^T (M=128 queries,
+//               N=64 keys) into one of two S buffers, and O += P.V (M=128, N=128 head dims) into
+//               the O accumulator; S for block i+2 is issued right after P.V of block i, so the
+//               tensor cores compute the next scores while the softmax of block i+1 runs;
+//   warps 2..5  softmax, one thread per query row (its TMEM lane): scores from TMEM, mask, online
+//               max / sum in fp32 with exp2 (scale folded into log2 e), rescale of the O row in
+//               TMEM when the max grows, P written as a swizzled f16 operand tile; at the end O
+//               divided by the row sum and stored.
+// SPLIT: every operand comes as f16 hi and lo planes (hi + lo = the f32 value) and each product is
+// lo.hi + hi.lo + hi.hi, P split the same way -- f32-accurate attention (the reference CPU build's
+// qwen3_attn_f32 / dit_attn_f32). Every wait is bounded; on a timeout the kernel records
+// ACB_DEVERR_TIMEOUT, stops, and still frees its TMEM.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "ptx.cuh"
+#include "tc.cuh"
+
+namespace acb {
+
+constexpr int kTcBQ      = 128;  // queries per CTA = TMEM lanes
+constexpr int kTcBK      = 64;   // keys per block
+constexpr int kTcD       = 128;  // head dim
+constexpr int kTcThreads = 192;
+
+enum { TC_MASK_NONE = 0, TC_MASK_CAUSAL = 1, TC_MASK_WINDOW = 2 };
+
+struct AttnTcArgs {
+    void *  o;
+    int     o_type;
+    int64_t o_ts;  // O element (b, i, h, d) at (b*Sq + i)*o_ts + h*128 + d
+    int     Sq, Skv, Nh, Nkv;
+    int     window, causal_off;
+    float   scale_log2;
+    int *   err;
+};
+
+template <bool SPLIT> struct TcLayout {
+    static constexpr int NP    = SPLIT ? 2 : 1;         // operand planes
+    static constexpr int QB    = NP * 2 * 16384;        // Q: plane x d-chunk x [128][64]
+    static constexpr int KB    = NP * 2 * 8192;         // K block: plane x d-chunk x [64][64]
+    static constexpr int VB    = NP * 16384;            // V^T block: plane x [128][64]
+    static constexpr int SB    = KB + VB;               // one ring stage
+    static constexpr int NS    = SPLIT ? 2 : 3;         // ring stages
+    static constexpr int PB    = NP * 16384;            // P: plane x [128][64]
+    static constexpr int TOTAL = QB + NS * SB + PB;     // 224 KB split, 144 KB otherwise
+};
+
+__device__ __forceinline__ bool tc_wait(uint64_t * bar, uint32_t parity, volatile int * abort_flag, int * err) {
+    if (*abort_flag) {
+        return false;
+    }
+    if (!ptx::mbar_wait(bar, parity)) {
+        *abort_flag = 1;
+        if (err) {
+            atomicOr(err, ACB_DEVERR_TIMEOUT);
+        }
+        return false;
+    }
+    return true;
+}
+
+template <int MASK, bool SPLIT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mql,
+                   const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mkl,
+                   const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mvl,
+                   const AttnTcArgs a) {
+    using Lay = TcLayout<SPLIT>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t * smem   = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t * sQ     = smem;
+    uint8_t * sStage = smem + Lay::QB;
+    uint8_t * sP     = sStage + Lay::NS * Lay::SB;
+    uint64_t * q_full   = reinterpret_cast<uint64_t *>(sP + Lay::PB);
+    uint64_t * kv_full  = q_full + 1;
+    uint64_t * kv_empty = kv_full + Lay::NS;
+    uint64_t * s_full   = kv_empty + Lay::NS;
+    uint64_t * p_full   = s_full + 2;
+    uint64_t * pv_done  = p_full + 1;
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(pv_done + 1);
+    __shared__ volatile int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int hk = h / (a.Nh / a.Nkv);
+    const int q0 = qt * kTcBQ;
+
+    // key blocks that the mask leaves for this query tile
+    int kb_lo = 0, kb_hi = (a.Skv + kTcBK - 1) / kTcBK;
+    if (MASK == TC_MASK_CAUSAL) {
+        const int last_q = min(q0 + kTcBQ, a.Sq) - 1 + a.causal_off;
+        kb_hi            = min(kb_hi, max(0, last_q / kTcBK + 1));
+    } else if (MASK == TC_MASK_WINDOW) {
+        kb_lo = max(0, (q0 - a.window) / kTcBK);
+        kb_hi = min(kb_hi, (min(q0 + kTcBQ, a.Sq) - 1 + a.window) / kTcBK + 1);
+    }
+    const int nblk = kb_hi > kb_lo ? kb_hi - kb_lo : 0;
+
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+        ptx::mbar_init(q_full, 1);
+        for (int s = 0; s < Lay::NS; s++) {
+            ptx::mbar_init(&kv_full[s], 1);
+            ptx::mbar_init(&kv_empty[s], 1);
+        }
+        ptx::mbar_init(&s_full[0], 1);
+        ptx::mbar_init(&s_full[1], 1);
+        ptx::mbar_init(p_full, 4);  // one arrival per softmax warp
+        ptx::mbar_init(pv_done, 1);
+        ptx::fence_mbar_init();
+        tma_prefetch_desc(&mq);
+        tma_prefetch_desc(&mk);
+        tma_prefetch_desc(&mv);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ptx::smem_u32(tmem_slot)),
+                     "r"(256));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    ptx::grid_dep_wait();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem  = *tmem_slot;
+    const uint32_t tO    = tmem + 128;  // S buffers at columns 0 and 64, O at 128..255
+
+    if (warp == 0) {
+        if (lane == 0 && nblk > 0) {
+            ptx::mbar_arrive_expect_tx(q_full, Lay::QB);
+            for (int p = 0; p < Lay::NP; p++) {
+                for (int c = 0; c < 2; c++) {
+                    tma_load_2d(sQ + (p * 2 + c) * 16384, p ? &mql : &mq, h * kTcD + c * 64, b * a.Sq + q0, q_full);
+                }
+            }
+            for (int i = 0; i < nblk; i++) {
+                const int s = i % Lay::NS;
+                if (i >= Lay::NS && !tc_wait(&kv_empty[s], ((i / Lay::NS) - 1) & 1, &abort_flag, a.err)) {
+                    break;
+                }
+                const int key0 = (kb_lo + i) * kTcBK;
+                uint8_t * st   = sStage + s * Lay::SB;
+                ptx::mbar_arrive_expect_tx(&kv_full[s], Lay::SB);
+                for (int p = 0; p < Lay::NP; p++) {
+                    for (int c = 0; c < 2; c++) {
+                        tma_load_2d(st + (p * 2 + c) * 8192, p ? &mkl : &mk, hk * kTcD + c * 64, b * a.Skv + key0,
+                                    &kv_full[s]);
+                    }
+                }
+                for (int p = 0; p < Lay::NP; p++) {
+                    tma_load_2d(st + Lay::KB + p * 16384, p ? &mvl : &mv, key0, (b * a.Nkv + hk) * kTcD, &kv_full[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && nblk > 0 && tc_wait(q_full, 0, &abort_flag, a.err)) {
+            constexpr uint32_t idesc_s = idesc_kind_f16(128, kTcBK, true);
+            constexpr uint32_t idesc_o = idesc_kind_f16(128, kTcD, true);
+            const uint32_t     q_addr  = ptx::smem_u32(sQ);
+            const uint32_t     p_addr  = ptx::smem_u32(sP);
+            // products (A plane, B plane): lo.hi + hi.lo + hi.hi (small terms first), or hi.hi
+            constexpr int      n_prod = SPLIT ? 3 : 1;
+            const int          pa[3]  = { SPLIT ? 1 : 0, 0, 0 };
+            const int          pb[3]  = { 0, SPLIT ? 1 : 0, 0 };
+            auto issue_s = [&](int i) -> bool {
+                const int s = i % Lay::NS;
+                if (!tc_wait(&kv_full[s], (i / Lay::NS) & 1, &abort_flag, a.err)) {
+                    return false;
+                }
+                tc_fence_after();
+                const uint32_t st  = ptx::smem_u32(sStage + s * Lay::SB);
+                const uint32_t tS  = tmem + (uint32_t) ((i & 1) * kTcBK);
+                uint32_t       acc = 0;
+                for (int pr = 0; pr < n_prod; pr++) {
+#pragma unroll
+                    for (int kk = 0; kk < kTcD / 16; kk++) {
+                        const int      c   = kk >> 2;
+                        const uint32_t off = (uint32_t) ((kk & 3) * 32);
+                        umma_f16kind(tS, smem_desc_sw128(q_addr + (pa[pr] * 2 + c) * 16384 + off),
+                                     smem_desc_sw128(st + (pb[pr] * 2 + c) * 8192 + off), idesc_s, acc);
+                        acc = 1;
+                    }
+                }
+                umma_commit(&s_full[i & 1]);
+                return true;
+            };
+            bool ok = issue_s(0) && (nblk < 2 || issue_s(1));
+            for (int i = 0; ok && i < nblk; i++) {
+                if (!tc_wait(p_full, i & 1, &abort_flag, a.err)) {
+                    break;
+                }
+                tc_fence_after();
+                const int      s   = i % Lay::NS;
+                const uint32_t vt  = ptx::smem_u32(sStage + s * Lay::SB + Lay::KB);
+                uint32_t       acc = i > 0 ? 1u : 0u;
+                for (int pr = 0; pr < n_prod; pr++) {
+#pragma unroll
+                    for (int kk = 0; kk < kTcBK / 16; kk++) {
+                        const uint32_t off = (uint32_t) (kk * 32);
+                        umma_f16kind(tO, smem_desc_sw128(p_addr + pa[pr] * 16384 + off),
+                                     smem_desc_sw128(vt + pb[pr] * 16384 + off), idesc_o, acc);
+                        acc = 1;
+                    }
+                }
+                umma_commit(pv_done);
+                umma_commit(&kv_empty[s]);  // K and V of this block are consumed
+                if (i + 2 < nblk) {
+                    ok = issue_s(i + 2);
+                }
+            }
+        }
+    } else {
+        // softmax: thread = query row (its TMEM lane)
+        const int      qq    = warp & 3;
+        const int      row   = qq * 32 + lane;
+        const int      iq    = q0 + row;  // query index within the sequence
+        const uint32_t lanes = (uint32_t) (qq * 32) << 16;
+        float          m = -INFINITY, l = 0.0f;
+        bool           ok = true;
+        for (int i = 0; i < nblk; i++) {
+            // every exit is warp-uniform: tcgen05.ld / st below are warp-collective
+            if (!__all_sync(0xffffffffu, tc_wait(&s_full[i & 1], (i >> 1) & 1, &abort_flag, a.err))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t r[64];
+            tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK), r);
+            tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK + 32), r + 32);
+            const int key0 = (kb_lo + i) * kTcBK;
+            float     mx   = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kTcBK; c++) {
+                const int j  = key0 + c;
+                bool      in = j < a.Skv;
+                if (MASK == TC_MASK_CAUSAL) {
+                    in = in && j <= iq + a.causal_off;
+                } else if (MASK == TC_MASK_WINDOW) {
+                    in = in && (iq > j ? iq - j : j - iq) <= a.window;
+                }
+                const float v = in ? __uint_as_float(r[c]) * a.scale_log2 : -INFINITY;
+                r[c]          = __float_as_uint(v);
+                mx            = fmaxf(mx, v);
+            }
+            const float m_new = fmaxf(m, mx);
+            const float alpha = (m == -INFINITY || m_new == -INFINITY) ? 1.0f : exp2f(m - m_new);
+            float       ls    = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kTcBK; c++) {
+                const float p = m_new == -INFINITY ? 0.0f : exp2f(__uint_as_float(r[c]) - m_new);
+                r[c]          = __float_as_uint(p);
+                ls += p;
+            }
+            if (i > 0) {
+                // the previous P.V has finished: O may be rescaled and P overwritten
+                if (!__all_sync(0xffffffffu, tc_wait(pv_done, (i - 1) & 1, &abort_flag, a.err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < kTcD / 32; c++) {
+                        uint32_t o[32];
+                        tmem_ld32(tO + lanes + (uint32_t) (c * 32), o);
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        }
+                        tmem_st32(tO + lanes + (uint32_t) (c * 32), o);
+                    }
+                }
+            }
+            l = l * alpha + ls;
+            m = m_new;
+            // P row into the swizzled [128][64] operand tile(s): 16-byte unit u of row `row` goes to
+            // unit u ^ (row % 8) (128-byte swizzle, rows 128 bytes apart)
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float  p0 = __uint_as_float(r[u * 8 + 2 * e]), p1 = __uint_as_float(r[u * 8 + 2 * e + 1]);
+                    const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
+                    __half2      hh = __halves2half2(h0, h1);
+                    hi[e]           = *reinterpret_cast<uint32_t *>(&hh);
+                    if (SPLIT) {
+                        __half2 ll = __floats2half2_rn(p0 - __half2float(h0), p1 - __half2float(h1));
+                        lo[e]      = *reinterpret_cast<uint32_t *>(&ll);
+                    }
+                }
+                const int off = row * 128 + ((u ^ (row & 7)) << 4);
+                *reinterpret_cast<uint4 *>(sP + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                if (SPLIT) {
+                    *reinterpret_cast<uint4 *>(sP + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                ptx::mbar_arrive(p_full);
+            }
+        }
+        if (ok && nblk > 0) {
+            ok = __all_sync(0xffffffffu, tc_wait(pv_done, (nblk - 1) & 1, &abort_flag, a.err));
+            tc_fence_after();
+        }
+        const float inv = (ok && l > 0.0f) ? 1.0f / l : 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < kTcD / 32; c++) {
+            uint32_t o[32];
+            if (nblk > 0 && ok) {
+                tmem_ld32(tO + lanes + (uint32_t) (c * 32), o);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    o[e] = 0u;
+                }
+            }
+            if (iq < a.Sq) {
+                const int64_t base = ((int64_t) b * a.Sq + iq) * a.o_ts + (int64_t) h * kTcD + c * 32;
+                if (a.o_type == ACB_TYPE_F32) {
+                    float4 * d = reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.o) + base);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        d[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
+                                           __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+                    }
+                } else {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float v0 = __uint_as_float(o[2 * e]) * inv, v1 = __uint_as_float(o[2 * e + 1]) * inv;
+                        if (a.o_type == ACB_TYPE_F16) {
+                            __half2 hh = __floats2half2_rn(v0, v1);
+                            pk[e]      = *reinterpret_cast<uint32_t *>(&hh);
+                        } else {
+                            __nv_bfloat162 bb = __floats2bfloat162_rn(v0, v1);
+                            pk[e]             = *reinterpret_cast<uint32_t *>(&bb);
+                        }
+                    }
+                    uint4 * d = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(a.o) + base);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        d[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+                    }
+                }
+            }
+        }
+    }
+    ptx::grid_dep_launch();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+    }
+}
+
+// V (f32 or f16, element (b, t, hk, d) at b*v_bs + t*v_ts + hk*128 + d) to V^T planes:
+// vt[((b*Nkv + hk)*128 + d)*vt_ld + t] = f16(v) and, with lo_off, vt[lo_off + same] = f16(v - hi).
+// A 32-token x 32-dim tile per block, transposed through shared memory.
+template <int TI>
+__global__ void __launch_bounds__(256) vt_planes_kernel(const void * __restrict__ v, int64_t v_bs, int64_t v_ts,
+                                                        int S, int Nkv, uint16_t * __restrict__ vt, int64_t vt_ld,
+                                                        int64_t lo_off) {
+    __shared__ float tile[32][33];
+    const int t0 = blockIdx.x * 32, dc = blockIdx.y, bh = blockIdx.z;  // bh = b*Nkv + hk; dc = 32-dim chunk
+    const int b = bh / Nkv, hk = bh - b * Nkv;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 8 rows per pass
+    using ei    = typename io<TI>::t;
+    const ei * src = reinterpret_cast<const ei *>(v) + (int64_t) b * v_bs + (int64_t) hk * kTcD + dc * 32;
+    for (int r = ty; r < 32; r += 8) {
+        const int t = t0 + r;
+        tile[r][tx] = t < S ? io<TI>::to_f(src[(int64_t) t * v_ts + tx]) : 0.0f;
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int t = t0 + tx;
+        if (t < S) {
+            const float   x   = tile[tx][r];
+            const __half  hi  = __float2half_rn(x);
+            const int64_t idx = ((int64_t) bh * kTcD + dc * 32 + r) * vt_ld + t;
+            vt[idx]           = __half_as_ushort(hi);
+            if (lo_off) {
+                vt[lo_off + idx] = __half_as_ushort(__float2half_rn(x - __half2float(hi)));
+            }
+        }
+    }
+}
+
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" acb_status acb_attn_vt(const void * v, int v_type, int64_t v_bs, int64_t v_ts, int batch, int S, int Nkv,
+                                  int head_dim, void * vt, int64_t vt_ld, int64_t lo_offset, acb_stream_t stream) {
+    if (!v || !vt || batch <= 0 || S <= 0 || Nkv <= 0 || vt_ld < S || lo_offset < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (head_dim != kTcD || (v_type != ACB_TYPE_F32 && v_type != ACB_TYPE_F16)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const dim3 grid((unsigned) ((S + 31) / 32), kTcD / 32, (unsigned) (batch * Nkv));
+    if (v_type == ACB_TYPE_F32) {
+        vt_planes_kernel<ACB_TYPE_F32><<<grid, 256, 0, (cudaStream_t) stream>>>(
+            v, v_bs, v_ts, S, Nkv, reinterpret_cast<uint16_t *>(vt), vt_ld, lo_offset);
+    } else {
+        vt_planes_kernel<ACB_TYPE_F16><<<grid, 256, 0, (cudaStream_t) stream>>>(
+            v, v_bs, v_ts, S, Nkv, reinterpret_cast<uint16_t *>(vt), vt_ld, lo_offset);
+    }
+    return launch_status();
+}
+
+extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, int64_t k_ts, const void * vt,
+                                  int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv,
+                                  int Nh, int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
+                                  int flags, int64_t q_lo, int64_t k_lo, int64_t vt_lo, int * err_flag,
+                                  acb_stream_t stream) {
+    if (!q || !k || !vt || !o || batch <= 0 || Sq <= 0 || Skv <= 0 || Nh <= 0 || Nkv <= 0 || Nh % Nkv != 0 ||
+        vt_ld < Skv) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (head_dim != kTcD || mask < 0 || mask > 2 ||
+        (o_type != ACB_TYPE_F32 && o_type != ACB_TYPE_BF16 && o_type != ACB_TYPE_F16)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const bool split = q_lo != 0 || k_lo != 0 || vt_lo != 0;
+    if (split && (q_lo == 0 || k_lo == 0 || vt_lo == 0)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    // TMA: 16-byte aligned bases and row strides; outputs of 16-byte units
+    if ((q_ts | k_ts | vt_ld | q_lo | k_lo | vt_lo) % 8 != 0 || o_ts % 8 != 0 ||
+        reinterpret_cast<uintptr_t>(q) % 16 || reinterpret_cast<uintptr_t>(k) % 16 ||
+        reinterpret_cast<uintptr_t>(vt) % 16 || reinterpret_cast<uintptr_t>(o) % 16) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const uint16_t * q16 = reinterpret_cast<const uint16_t *>(q);
+    const uint16_t * k16 = reinterpret_cast<const uint16_t *>(k);
+    const uint16_t * v16 = reinterpret_cast<const uint16_t *>(vt);
+    CUtensorMap      mq, mql, mk, mkl, mv, mvl;
+    const int64_t    qc = (int64_t) Nh * kTcD, kc = (int64_t) Nkv * kTcD;
+    bool ok = make_map_2d(&mq, q16, true, qc, (int64_t) batch * Sq, q_ts, 64, kTcBQ) &&
+              make_map_2d(&mk, k16, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
+              make_map_2d(&mv, v16, true, Skv, (int64_t) batch * Nkv * kTcD, vt_ld, 64, kTcD);
+    if (split) {
+        ok = ok && make_map_2d(&mql, q16 + q_lo, true, qc, (int64_t) batch * Sq, q_ts, 64, kTcBQ) &&
+             make_map_2d(&mkl, k16 + k_lo, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
+             make_map_2d(&mvl, v16 + vt_lo, true, Skv, (int64_t) batch * Nkv * kTcD, vt_ld, 64, kTcD);
+    } else {
+        mql = mq;
+        mkl = mk;
+        mvl = mv;
+    }
+    if (!ok) {
+        return ACB_ERR_CUDA;
+    }
+    AttnTcArgs a = {};
+    a.o          = o;
+    a.o_type     = o_type;
+    a.o_ts       = o_ts;
+    a.Sq         = Sq;
+    a.Skv        = Skv;
+    a.Nh         = Nh;
+    a.Nkv        = Nkv;
+    a.window     = window;
+    a.causal_off = causal_off;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.err        = err_flag;
+    const size_t smem = (size_t) (split ? TcLayout<true>::TOTAL : TcLayout<false>::TOTAL) + 1024 + 256;
+    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                 const CUtensorMap, const AttnTcArgs) = nullptr;
+#define ACB_TC_PICK(M) kern = split ? attn_tc_kernel<M, true> : attn_tc_kernel<M, false>
+    if (mask == TC_MASK_CAUSAL) {
+        ACB_TC_PICK(TC_MASK_CAUSAL);
+    } else if (mask == TC_MASK_WINDOW) {
+        ACB_TC_PICK(TC_MASK_WINDOW);
+    } else {
+        ACB_TC_PICK(TC_MASK_NONE);
+    }
+#undef ACB_TC_PICK
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) ((Sq + kTcBQ - 1) / kTcBQ), (unsigned) Nh, (unsigned) batch);
+    cfg.blockDim           = dim3(kTcThreads);
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = (cudaStream_t) stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = (flags & ACB_FLAG_PDL) ? attr : nullptr;
+    cfg.numAttrs                                       = (flags & ACB_FLAG_PDL) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mq, mql, mk, mkl, mv, mvl, a);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}

@@ -15,10 +15,10 @@
 // still frees its TMEM.
 #include <cuda.h>
 
-#include <mutex>
 
 #include "common.cuh"
 #include "ptx.cuh"
+#include "tc.cuh"
 
 namespace acb {
 
@@ -48,71 +48,6 @@ struct GemmArgs {
     int           kps;     // k-tiles per split
     float *       ws;      // [splits][M][N] f32 partial accumulators
 };
-
-// ---- tcgen05 / TMA helpers ------------------------------------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * map, int x, int y, uint64_t * bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            ptx::smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(ptx::smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap * map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart (SM100 shared-memory descriptor:
-// start >> 4 at [0,14), stride byte offset >> 4 at [32,46), version 1 at [46,48), layout 2 at [61,64)).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-    return (uint64_t) ((saddr & 0x3FFFF) >> 4) | ((uint64_t) (1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
-}
-
-// kind::f16 instruction descriptor: fp32 accumulate (bits 4-5 = 1), A and B both bf16 (bits
-// 7-9 and 10-12 = 1) or both f16 (0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-__host__ __device__ constexpr uint32_t idesc_kind_f16(int M, int N, bool f16) {
-    return (1u << 4) | (f16 ? 0u : ((1u << 7) | (1u << 10))) | ((uint32_t) (N >> 3) << 17) |
-           ((uint32_t) (M >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16kind(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t * bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     ptx::smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t * r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
-        "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void flag_timeout(int * err) {
-    if (err) {
-        atomicOr(err, ACB_DEVERR_TIMEOUT);
-    }
-}
 
 // 32 accumulator columns of one row to a 16-bit C (vector stores when whole and aligned)
 template <int T>
@@ -415,39 +350,10 @@ static int choose_splits(int64_t M, int64_t N, int64_t K, int * kps) {
     return (k_tiles + *kps - 1) / *kps;
 }
 
-// ---- host: tensor maps through the driver entry point (no libcuda link) ----------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *                          p  = nullptr;
-        cudaDriverEntryPointQueryResult qr = cudaDriverEntryPointSymbolNotFound;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qr) == cudaSuccess &&
-            qr == cudaDriverEntryPointSuccess) {
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-        }
-    });
-    return fn;
-}
-
-// 16-bit row-major [rows][ld] (K contiguous), box = box_rows x 64 elements, 128-byte swizzle
+// bf16/f16 row-major [rows][ld] (K contiguous), box = box_rows x 64 elements, 128-byte swizzle
 static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K, int64_t ld, int box_rows,
                      bool f16) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) {
-        return false;
-    }
-    const cuuint64_t dims[2]    = { (cuuint64_t) K, (cuuint64_t) rows };
-    const cuuint64_t strides[1] = { (cuuint64_t) (ld * 2) };
-    const cuuint32_t box[2]     = { (cuuint32_t) kBK, (cuuint32_t) box_rows };
-    const cuuint32_t estr[2]    = { 1, 1 };
-    return fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return make_map_2d(m, base, f16, K, rows, ld, kBK, box_rows);
 }
 
 }  // namespace acb

@@ -243,6 +243,23 @@ ACB_API acb_status acb_attn_prefill_split(const void * q, int64_t q_bs, int64_t 
                                           int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
                                           int flags, int64_t q_lo, int64_t k_lo, int64_t v_lo, acb_stream_t stream);
 
+/* Attention on the 5th-generation tensor cores (tcgen05.mma into TMEM, TMA-fed 128-byte-swizzled
+ * tiles, one softmax thread per query row): the same results as acb_attn_prefill for sequences
+ * stored batch after batch. q [batch*Sq][q_ts] and k [batch*Skv][k_ts] f16 (head h at column
+ * h*128; q_ts, k_ts multiples of 8); V is given transposed, vt [batch][Nkv][128][vt_ld] f16
+ * (acb_attn_vt, vt_ld >= Skv, a multiple of 8); o [batch*Sq][o_ts] f32, bf16 or f16. With q_lo /
+ * k_lo / vt_lo nonzero every operand has an f16 lo plane that many elements further and the
+ * products are lo.hi + hi.lo + hi.hi: f32-accurate attention. Masks as acb_attn_prefill. */
+ACB_API acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, int64_t k_ts, const void * vt,
+                               int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
+                               int Nkv, int head_dim, int mask, int window, int causal_off, float scale, int flags,
+                               int64_t q_lo, int64_t k_lo, int64_t vt_lo, int * err_flag, acb_stream_t stream);
+/* V (f32 or f16; element (b, t, hk, d) at b*v_bs + t*v_ts + hk*128 + d) to the transposed f16
+ * operand of acb_attn_tc: vt[((b*Nkv + hk)*128 + d)*vt_ld + t]; with lo_offset nonzero also the lo
+ * plane f16(v - hi) at lo_offset elements further. */
+ACB_API acb_status acb_attn_vt(const void * v, int v_type, int64_t v_bs, int64_t v_ts, int batch, int S, int Nkv,
+                               int head_dim, void * vt, int64_t vt_ld, int64_t lo_offset, acb_stream_t stream);
+
 /* ---- DiT step kernels (configs 4 and 5) ------------------------------------------------------ */
 
 /* tt = {t, t_r} on the device: out[0][:] = ggml_timestep_embedding(t*1000, dim, max_period),

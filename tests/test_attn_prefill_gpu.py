@@ -130,3 +130,62 @@ def test_attn_prefill_split_is_fp32_accurate(cuda, B, Sq, Skv, Nh, Nkv, mask, wi
     got, want = o.double().cpu().numpy(), ref.cpu().numpy()
     for b in range(B):
         assert max_rel(got[b], want[b]) <= 1e-5, (b, max_rel(got[b], want[b]))
+
+
+TC_CASES = [
+    (1, 256, 256, 16, 8, acb.MASK_CAUSAL, 0, 0),
+    (8, 750, 750, 16, 8, acb.MASK_WINDOW, 128, 0),
+    (8, 750, 750, 16, 8, acb.MASK_NONE, 0, 0),
+    (8, 750, 512, 16, 8, acb.MASK_NONE, 0, 0),
+    (2, 77, 33, 4, 2, acb.MASK_NONE, 0, 0),
+    (1, 100, 300, 16, 8, acb.MASK_CAUSAL, 0, 200),
+]
+
+
+@pytest.mark.parametrize("B,Sq,Skv,Nh,Nkv,mask,window,causal_off", TC_CASES)
+def test_attn_tc_matches_reference(cuda, B, Sq, Skv, Nh, Nkv, mask, window, causal_off):
+    """acb_attn_tc (tcgen05): f16 operands against the fp32 attention of the same f16 values
+    (cosine >= 0.99999, max_rel <= 2e-3); hi/lo split operands against float64 attention of the
+    f32 values (max_rel <= 1e-5) and against the mma.sync split kernel."""
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(Sq * 7 + Skv + mask)
+    q = torch.randn(B, Sq, Nh * 128, device=cuda, generator=g) * 1.5
+    k = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g) * 1.5
+    v = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    # f16 operands
+    qh, kh, vh = q.half(), k.half(), v.half()
+    vt, ld, _ = acb.attn_vt(vh, Nkv)
+    o = acb.attn_tc(qh.view(B * Sq, -1), kh.view(B * Skv, -1), vt, ld, Nh, Nkv, Sq, Skv, B, mask=mask, window=window,
+                    causal_off=causal_off, err=err)
+    ref = torch_ref(qh, kh, vh, Nh, Nkv, mask, window, causal_off).reshape(B * Sq, -1)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got, want = o.view(B, Sq, -1).cpu().numpy(), ref.view(B, Sq, -1).cpu().numpy()
+    for b in range(B):
+        c, r = cos_sim(got[b], want[b]), max_rel(got[b], want[b])
+        assert c >= 0.99999 and r <= 2e-3, ("f16", b, c, r)
+    # hi/lo split operands
+    def planes(t):
+        flat = t.reshape(-1, t.shape[-1])
+        pl = acb.act_quant_ex(flat, flat.shape[1], acb.F16, acb.LAYOUT_PLANES)
+        return pl, flat.numel()
+    qp, qlo = planes(q)
+    kp, klo = planes(k)
+    vts, ld, vlo = acb.attn_vt(v, Nkv, lo=True)
+    o2 = acb.attn_tc(qp[: B * Sq], kp[: B * Skv], vts, ld, Nh, Nkv, Sq, Skv, B, mask=mask, window=window,
+                     causal_off=causal_off, q_lo=qlo, k_lo=klo, vt_lo=vlo, err=err)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    ref2 = torch_ref(q.double(), k.double(), v.double(), Nh, Nkv, mask, window, causal_off)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got2, want2 = o2.view(B, Sq, -1).double().cpu().numpy(), ref2.cpu().numpy()
+    for b in range(B):
+        assert max_rel(got2[b], want2[b]) <= 1e-5, ("split", b, max_rel(got2[b], want2[b]))
+    if causal_off == 0:
+        hq = qp[: B * Sq].view(B, Sq, -1)
+        hk = kp[: B * Skv].view(B, Skv, -1)
+        vp, _ = planes(v)
+        hv = vp[: B * Skv].view(B, Skv, -1)
+        o3 = acb.attn_prefill_split(hq, hk, hv, qlo, klo, v.numel(), Nh, Nkv, mask=mask, window=window)
+        assert max_rel(o2.view(B, Sq, -1).cpu().numpy(), o3.cpu().numpy()) <= 1e-5
