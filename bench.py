@@ -585,8 +585,8 @@ ATTN_SHAPES = [("dit_self_window", 8, 750, 750, 2, 128), ("dit_self_full", 8, 75
 
 
 def run_attn_shapes(dev, reps=10, which=None):
-    """acb_attn_prefill (f16 operands) and acb_attn_prefill_split (hi/lo planes, the exact mode)
-    per attention shape of configs 1 and 4 (16 q heads, 8 kv heads, D 128), CUDA events around
+    """acb_attn_prefill (mma.sync; f16 operands, and hi/lo planes of the exact mode) and acb_attn_tc
+    (tcgen05; the same two operand forms) per attention shape of configs 1 and 4 (16 q heads, 8 kv heads, D 128), CUDA events around
     `reps` launches after 3 warm-ups; algorithmic TFLOP/s (QK^T and PV over the unmasked pairs)."""
     import torch
 
@@ -605,17 +605,26 @@ def run_attn_shapes(dev, reps=10, which=None):
         hi = [p[: p.shape[0] // 2].view(t.shape) for p, t in zip(planes, (q, k, v))]
         lo = [t.numel() for t in (q, k, v)]
         o = torch.empty(B, Sq, Nh * D, device=dev)
+        vt_h, vld, _ = acb.attn_vt(hi[2], Nkv)
+        vt_s, _, vlo = acb.attn_vt(v, Nkv, lo=True)
+        qf, kf = planes[0], planes[1]
         pairs = sum(min(Skv, i + win + 1) - max(0, i - win) for i in range(Sq)) if mask == 2 else \
             (Sq * (Sq + 1) // 2 if mask == 1 else Sq * Skv)
         fl = 4.0 * D * Nh * B * pairs
         res = {"B": B, "Sq": Sq, "Skv": Skv, "mask": mask}
-        for mode in ("f16", "split"):
+        for mode in ("f16", "split", "tc_f16", "tc_split"):
             def call():
                 if mode == "f16":
                     acb.attn_prefill(hi[0], hi[1], hi[2], Nh, Nkv, mask=mask, window=win, out=o)
-                else:
+                elif mode == "split":
                     acb.attn_prefill_split(hi[0], hi[1], hi[2], lo[0], lo[1], lo[2], Nh, Nkv, mask=mask,
                                            window=win, out=o)
+                elif mode == "tc_f16":
+                    acb.attn_tc(qf[: B * Sq], kf[: B * Skv], vt_h, vld, Nh, Nkv, Sq, Skv, B, mask=mask, window=win,
+                                out=o.view(B * Sq, -1))
+                else:
+                    acb.attn_tc(qf[: B * Sq], kf[: B * Skv], vt_s, vld, Nh, Nkv, Sq, Skv, B, mask=mask, window=win,
+                                out=o.view(B * Sq, -1), q_lo=lo[0], k_lo=lo[1], vt_lo=vlo)
             for _ in range(3):
                 call()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

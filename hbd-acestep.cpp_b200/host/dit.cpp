@@ -69,9 +69,12 @@ struct acb_dit {
     // per-shape scratch
     int    Ng = 0, S = 0, enc_S = 0;
     DevBuf tt, sinus, th1, th2, temb2, tproj2, ada, out_ss;
-    DevBuf input, h, xn, xq, qkv32, qkv16, planes, q16, k16, att, gu, vel, pos, rope, ws, err;
-    DevBuf enc_in, enc_h, kv32, kvcache;  // condition: raw [Ng][enc_S][H_enc], embedded, per-layer K/V planes
-    size_t kv_layer_elems = 0;            // elements of one plane of one layer's cached K||V
+    DevBuf input, h, xn, xq, qkv32, qkv16, planes, vtb, q16, k16, att, gu, vel, pos, rope, ws, err;
+    DevBuf enc_in, enc_h, kv32, kvcache;  // condition: raw [Ng][enc_S][H_enc], embedded, per-layer K / V^T planes
+    // cached condition of one layer: K hi, K lo ([Ng*enc_S][KD] each), V^T hi, V^T lo
+    // ([Ng][Nkv][128][enc_ld] each)
+    size_t k_plane = 0, vt_plane = 0, kv_layer_elems = 0;
+    int    s_ld = 0, enc_ld = 0;  // V^T row lengths: sequence / condition rows rounded up to 8
     int    eval_kernels   = 0;            // kernel launches of one captured evaluation
     // generate
     DevBuf                          xt, vt, out, ra;
@@ -134,7 +137,10 @@ acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
     A(xq, std::max(R, Re) * XQ * 2);
     A(qkv32, R * NQKV * 4);
     A(qkv16, R * NQKV * 2);
-    A(planes, 2 * std::max(R * NQKV, Re * 2 * KD) * 2);
+    s_ld   = (S + 7) / 8 * 8;
+    enc_ld = (enc_S + 7) / 8 * 8;
+    A(planes, 2 * R * (QD + KD) * 2);
+    A(vtb, 2 * (size_t) Ng * KD * s_ld * 2);
     A(q16, R * QD * 2);
     A(k16, R * KD * 2);
     A(att, R * QD * 4);
@@ -143,8 +149,10 @@ acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
     A(enc_in, Re * c.enc_hidden_size * 4);
     A(enc_h, Re * H * 4);
     A(kv32, Re * 2 * KD * 4);
-    kv_layer_elems = Re * 2 * KD;
-    A(kvcache, (size_t) c.n_layers * 2 * kv_layer_elems * 2);
+    k_plane        = Re * KD;
+    vt_plane       = (size_t) Ng * KD * enc_ld;
+    kv_layer_elems = 2 * (k_plane + vt_plane);
+    A(kvcache, (size_t) c.n_layers * kv_layer_elems * 2);
     if (!err.p) {
         A(err, 4, true);
     }
@@ -231,9 +239,11 @@ acb_status acb_dit::condition(cudaStream_t s) {
         ACB_TRY(acb_qk_norm_rope(kv, ACB_TYPE_F32, 2 * KD, kv, ACB_TYPE_F32, 2 * KD, D, 0, Re, c.n_kv_heads, D,
                                  (const float *) L.ca_k_norm->data, c.rms_norm_eps, nullptr, nullptr, 0, err.as<int>(),
                                  as));
-        uint16_t * hi = kvcache.as<uint16_t>() + (size_t) l * 2 * kv_layer_elems;
-        ACB_TRY(acb_act_quant_ex(kv, 2 * KD, 0, Re, 2 * KD, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, 2 * KD,
-                                 (int64_t) kv_layer_elems, as));
+        uint16_t * kh = kvcache.as<uint16_t>() + (size_t) l * kv_layer_elems;
+        ACB_TRY(acb_act_quant_ex(kv, 2 * KD, 0, Re, KD, ACB_TYPE_F16, ACB_LAYOUT_PLANES, kh, ACB_TYPE_F16, KD,
+                                 (int64_t) k_plane, as));
+        ACB_TRY(acb_attn_vt(kv + KD, ACB_TYPE_F32, (int64_t) enc_S * 2 * KD, 2 * KD, Ng, enc_S, c.n_kv_heads, D,
+                            kh + 2 * k_plane, enc_ld, (int64_t) vt_plane, as));
     }
     return ACB_OK;
 }
@@ -272,13 +282,15 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
         ACB_TRY(acb_qk_norm_rope(q32 + QD, ACB_TYPE_F32, NQKV, q32 + QD, ACB_TYPE_F32, NQKV, D, 0, R, Nkv, D,
                                  (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
                                  as));
-        const int64_t lo = (int64_t) R * NQKV;
+        // hi/lo planes of Q||K, and V transposed into hi/lo planes, for the tensor-core attention
+        const int64_t W  = QD + KD;
+        const int64_t lo = (int64_t) R * W;
         uint16_t *    hi = planes.as<uint16_t>();
-        ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, R, NQKV, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, NQKV, lo,
-                                 as));
-        ACB_TRY(acb_attn_prefill_split(hi, (int64_t) S * NQKV, NQKV, hi + QD, (int64_t) S * NQKV, NQKV, hi + QD + KD,
-                                       (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng, S, S,
-                                       Nh, Nkv, D, mask, c.sliding_window, 0, scale, kPdl, lo, lo, lo, as));
+        const int64_t vl = (int64_t) Ng * KD * s_ld;
+        ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, R, W, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, W, lo, as));
+        ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, vl, as));
+        ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, Ng, S, S, Nh, Nkv, D, mask,
+                            c.sliding_window, 0, scale, kPdl, lo, lo, vl, e, as));
     } else {
         uint16_t * q16p = qkv16.as<uint16_t>();
         ACB_TRY(dense_forward(L.sa_qkv, false, xp, H, 0, R, q16p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
@@ -289,9 +301,9 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
         ACB_TRY(acb_qk_norm_rope(q16p + QD, ACB_TYPE_F16, NQKV, k16.p, ACB_TYPE_F16, KD, D, 0, R, Nkv, D,
                                  (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
                                  as));
-        ACB_TRY(acb_attn_prefill(q16.p, (int64_t) S * QD, QD, k16.p, (int64_t) S * KD, KD, q16p + QD + KD,
-                                 (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng, S, S, Nh,
-                                 Nkv, D, mask, c.sliding_window, 0, scale, kPdl | ACB_FLAG_F16, as));
+        ACB_TRY(acb_attn_vt(q16p + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, 0, as));
+        ACB_TRY(acb_attn_tc(q16.p, QD, k16.p, KD, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, Ng, S, S, Nh, Nkv, D, mask,
+                            c.sliding_window, 0, scale, kPdl, 0, 0, 0, e, as));
     }
     ACB_TRY(dense_forward(L.sa_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0, R,
                           sc, s));
@@ -302,20 +314,18 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ACB_TRY(dense_forward(L.ca_q, exact, xp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc, s));
     ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, cq, ACB_TYPE_F32, QD, D, 0, R, Nh, D,
                              (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
-    const uint16_t * kv_hi = kvcache.as<uint16_t>() + (size_t) l * 2 * kv_layer_elems;
-    const int64_t    kvlo  = (int64_t) kv_layer_elems;
+    const uint16_t * k_hi  = kvcache.as<uint16_t>() + (size_t) l * kv_layer_elems;
+    const uint16_t * vt_hi = k_hi + 2 * k_plane;
     if (exact) {
         const int64_t lo = (int64_t) R * QD;
         uint16_t *    qh = planes.as<uint16_t>();
         ACB_TRY(acb_act_quant_ex(cq, QD, 0, R, QD, ACB_TYPE_F16, ACB_LAYOUT_PLANES, qh, ACB_TYPE_F16, QD, lo, as));
-        ACB_TRY(acb_attn_prefill_split(qh, (int64_t) S * QD, QD, kv_hi, (int64_t) enc_S * 2 * KD, 2 * KD, kv_hi + KD,
-                                       (int64_t) enc_S * 2 * KD, 2 * KD, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng,
-                                       S, enc_S, Nh, Nkv, D, 0, 0, 0, scale, kPdl, lo, kvlo, kvlo, as));
+        ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
+                            0, scale, kPdl, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
     } else {
         ACB_TRY(acb_act_quant(cq, QD, R, QD, ACB_TYPE_F16, q16.p, ACB_TYPE_F16, QD, as));
-        ACB_TRY(acb_attn_prefill(q16.p, (int64_t) S * QD, QD, kv_hi, (int64_t) enc_S * 2 * KD, 2 * KD, kv_hi + KD,
-                                 (int64_t) enc_S * 2 * KD, 2 * KD, att.p, ACB_TYPE_F32, (int64_t) S * QD, QD, Ng, S,
-                                 enc_S, Nh, Nkv, D, 0, 0, 0, scale, kPdl | ACB_FLAG_F16, as));
+        ACB_TRY(acb_attn_tc(q16.p, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0,
+                            0, 0, scale, kPdl, 0, 0, 0, e, as));
     }
     ACB_TRY(dense_forward(L.ca_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
                           sc, s));

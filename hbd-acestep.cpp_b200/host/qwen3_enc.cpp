@@ -57,7 +57,8 @@ struct acb_qwen3_enc {
 
     // scratch for up to cap tokens
     int                            cap = 0;
-    DevBuf                         ids, pos, rope, h, xn, xq, qkv, qkv32, planes, q, k, att, gu, out, err, ws;
+    DevBuf                         ids, pos, rope, h, xn, xq, qkv, qkv32, planes, vtb, q, k, att, gu, out, err, ws;
+    int                            s_ld = 0;  // V^T row length: cap rounded up to 8
     std::map<int, cudaGraphExec_t> graphs;  // one per S * 2 + exact
 
     ~acb_qwen3_enc() {
@@ -101,7 +102,9 @@ acb_status acb_qwen3_enc::reserve(int S) {
     bad |= xq.alloc((size_t) n * XQ * 3 * 2) != ACB_OK;
     bad |= qkv.alloc((size_t) n * nqkv() * 2) != ACB_OK;
     bad |= qkv32.alloc((size_t) n * nqkv() * 4) != ACB_OK;
-    bad |= planes.alloc((size_t) n * nqkv() * 2 * 2) != ACB_OK;
+    bad |= planes.alloc((size_t) n * (QD + KD) * 2 * 2) != ACB_OK;
+    s_ld = (n + 7) / 8 * 8;
+    bad |= vtb.alloc((size_t) 2 * KD * s_ld * 2) != ACB_OK;
     bad |= q.alloc((size_t) n * QD * 2) != ACB_OK;
     bad |= k.alloc((size_t) n * KD * 2) != ACB_OK;
     bad |= att.alloc((size_t) n * QD * 4) != ACB_OK;
@@ -170,14 +173,16 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
             ACB_TRY(acb_qk_norm_rope(q32 + QD, ACB_TYPE_F32, NQKV, q32 + QD, ACB_TYPE_F32, NQKV, D, 0, S, Nkv, D,
                                      (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
                                      as));
-            const int64_t lo = (int64_t) cap * NQKV;
+            // hi/lo planes of Q||K and of V^T for the tensor-core attention
+            const int64_t W  = QD + KD;
+            const int64_t lo = (int64_t) cap * W;
+            const int64_t vl = (int64_t) KD * s_ld;
             uint16_t *    hi = planes.as<uint16_t>();
-            ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, S, NQKV, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, NQKV, lo,
-                                     as));
-            ACB_TRY(acb_attn_prefill_split(hi, (int64_t) S * NQKV, NQKV, hi + QD, (int64_t) S * NQKV, NQKV,
-                                           hi + QD + KD, (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32,
-                                           (int64_t) S * QD, QD, 1, S, S, Nh, Nkv, D, mask, 0, 0, scale, kPdl, lo, lo,
-                                           lo, as));
+            ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, S, W, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, W, lo, as));
+            ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D, vtb.p, s_ld, vl,
+                                as));
+            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, 1, S, S, Nh, Nkv, D, mask, 0,
+                                0, scale, kPdl, lo, lo, vl, e, as));
         } else {
             ACB_TRY(dense_forward(L.qkv, false, xp, H, 0, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
                                   0, sc, s));
@@ -187,10 +192,10 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
             ACB_TRY(acb_qk_norm_rope(qkv.as<uint16_t>() + QD, ACB_TYPE_F16, NQKV, k.p, ACB_TYPE_F16, KD, D, 0, S, Nkv,
                                      D, (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap,
                                      e, as));
-            ACB_TRY(acb_attn_prefill(q.p, (int64_t) S * QD, QD, k.p, (int64_t) S * KD, KD,
-                                     qkv.as<uint16_t>() + QD + KD, (int64_t) S * NQKV, NQKV, att.p, ACB_TYPE_F32,
-                                     (int64_t) S * QD, QD, 1, S, S, Nh, Nkv, D, mask, 0, 0, scale, kPdl | ACB_FLAG_F16,
-                                     as));
+            ACB_TRY(acb_attn_vt(qkv.as<uint16_t>() + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D,
+                                vtb.p, s_ld, 0, as));
+            ACB_TRY(acb_attn_tc(q.p, QD, k.p, KD, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+                                scale, kPdl, 0, 0, 0, e, as));
         }
         ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
                               0, sc, s));
