@@ -122,6 +122,7 @@ def lib():
             "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
             "acb_vec_dot_type": (I, [I]),
             "acb_gemm_workspace_bytes": (C.c_size_t, [I64, I64, I64]),
+            "acb_gemm_pair_clusters": (I, [I]),
             "acb_gemm_tc": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, C.c_size_t, P,
                                 P]),
         }
@@ -408,6 +409,11 @@ def gemm_workspace_bytes(M, N, K) -> int:
 
 MASK_NONE, MASK_CAUSAL, MASK_WINDOW = 0, 1, 2
 
+
+
+def gemm_pair_clusters(f16=False):
+    """CTA pairs the GEMM runs on at once (0: the pair kernel is off)."""
+    return int(lib().acb_gemm_pair_clusters(1 if f16 else 0))
 
 def attn_prefill(q, k, v, Nh, Nkv, mask=MASK_NONE, window=0, causal_off=0, out=None, out_dtype=None, scale=None,
                  flags=0, stream=None):

@@ -2,19 +2,27 @@
 // every ggml_mul_mat of dit_ggml_build_layer at M = tokens):
 //     C[m][n] = epilogue( sum_k A[m][k] * B[n][k] ),  A, B bf16 or f16 K-major, fp32 accumulation.
 //
-// sm_100a design (one persistent CTA per SM, 6 warps, no clusters, no multicast):
-//   warp 0      TMA producer: A tile 128x64 and B tile 256x64 per stage (128-byte swizzle) into a
-//               4-stage ring (48 KB per stage), completion on an mbarrier per stage;
-//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators), one elected thread
-//               issues tcgen05.mma (M=128, N=256, K=16; kind::f16 with bf16 or f16 inputs) and releases
-//               ring stages / publishes finished accumulators with tcgen05.commit;
+// sm_100a design (persistent, 6 warps, no multicast loads). Two variants of one kernel:
+//   single CTA  work tile 128x256: A 128x64 + B 256x64 per stage (48 KB), 4-stage ring;
+//   CTA pair    work tile 256x256 on a cluster of two CTAs (tcgen05 cta_group::2): each CTA loads
+//               its own 128 rows of A and its half (128 rows) of B per stage (32 KB), 6-stage ring;
+//               the leader CTA issues M=256 MMAs that read B from both CTAs' shared memory and
+//               write each CTA's 128 rows into that CTA's TMEM. Per SM this moves 2/3 of the
+//               shared-memory bytes of the single-CTA tile for the same tensor work.
+//   warp 0      TMA producer (128-byte swizzle), completion on an mbarrier per stage (the
+//               leader's, for a pair: both CTAs' bytes count there);
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators); one elected thread
+//               (the leader's, for a pair) issues tcgen05.mma (K=16, kind::f16, bf16 or f16
+//               inputs) and releases ring stages / publishes finished accumulators with
+//               tcgen05.commit (to both CTAs of a pair);
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM lane quarter, fused
 //               bias / residual / DiT gated residual, f32, bf16 or f16 stores; the accumulator is
-//               handed back so the MMA of the next tile overlaps this epilogue.
+//               handed back (to the leader, for a pair) so the next tile's MMA overlaps it.
 // Every mbarrier wait is bounded; on a timeout the kernel records ACB_DEVERR_TIMEOUT, stops, and
-// still frees its TMEM.
+// still frees its TMEM (both CTAs of a pair meet at a cluster barrier first).
 #include <cuda.h>
 
+#include <cstdlib>
 
 #include "common.cuh"
 #include "ptx.cuh"
@@ -22,12 +30,20 @@
 
 namespace acb {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kStages = 4;
-constexpr int kATile = kBM * kBK * 2;  // 16 KB
-constexpr int kBTile = kBN * kBK * 2;  // 32 KB
-constexpr int kStageBytes = kATile + kBTile;
+constexpr int kBN = 256, kBK = 64;
 constexpr int kGemmThreads = 192;
 constexpr int kTmemCols    = 512;
+
+template <bool PAIR> struct GemmCfg {
+    static constexpr int      kTileM  = PAIR ? 256 : 128;  // output rows per work tile
+    static constexpr int      kRowsB  = PAIR ? 128 : 256;  // B rows loaded per CTA
+    static constexpr int      kATile  = 128 * kBK * 2;     // 16 KB
+    static constexpr int      kBTile  = kRowsB * kBK * 2;
+    static constexpr int      kStage  = kATile + kBTile;
+    static constexpr int      kStages = PAIR ? 6 : 4;
+    static constexpr uint32_t kTx     = (PAIR ? 2 : 1) * kStage;  // bytes landing per stage
+    static constexpr size_t   kSmem   = (size_t) kStages * kStage + 1024 + 256;
+};
 
 enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RES = 2, EPI_GATED_RES = 4 };
 
@@ -72,82 +88,108 @@ __device__ __forceinline__ void store_row16(void * C, int64_t off, const float *
 }
 
 // ---- the kernel ------------------------------------------------------------------------------------
-template <bool F16>
+template <bool F16, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const GemmArgs g) {
+    using Cf = GemmCfg<PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t * ring = smem;  // kStages * kStageBytes, 1024-aligned tiles
-    uint64_t * full       = reinterpret_cast<uint64_t *>(smem + kStages * kStageBytes);
-    uint64_t * empty      = full + kStages;
-    uint64_t * tmem_full  = empty + kStages;
+    uint8_t * ring = smem;  // kStages * kStage, 1024-aligned tiles (same offsets in both CTAs of a pair)
+    uint64_t * full       = reinterpret_cast<uint64_t *>(smem + Cf::kStages * Cf::kStage);
+    uint64_t * empty      = full + Cf::kStages;
+    uint64_t * tmem_full  = empty + Cf::kStages;
     uint64_t * tmem_empty = tmem_full + 2;
     uint32_t * tmem_slot  = reinterpret_cast<uint32_t *>(tmem_empty + 2);
     __shared__ volatile int abort_flag;
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m_tiles = (g.M + kBM - 1) / kBM, n_tiles = (g.N + kBN - 1) / kBN;
+    const int      warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank   = PAIR ? cluster_ctarank() : 0;
+    const bool     leader = rank == 0;
+    const int64_t  unit    = PAIR ? (blockIdx.x >> 1) : blockIdx.x;  // work-issuing unit: CTA or CTA pair
+    const int64_t  n_units = PAIR ? (gridDim.x >> 1) : gridDim.x;
+    const int64_t m_tiles = (g.M + Cf::kTileM - 1) / Cf::kTileM, n_tiles = (g.N + kBN - 1) / kBN;
     const int64_t tiles   = m_tiles * n_tiles;
     const int64_t n_work  = tiles * g.splits;
     const int     k_tiles = (int) (g.K / kBK);
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < Cf::kStages; s++) {
             ptx::mbar_init(&full[s], 1);
             ptx::mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; a++) {
             ptx::mbar_init(&tmem_full[a], 1);
-            ptx::mbar_init(&tmem_empty[a], 4);  // one arrival per epilogue warp
+            ptx::mbar_init(&tmem_empty[a], PAIR ? 8 : 4);  // one arrival per epilogue warp (of both CTAs)
         }
         ptx::fence_mbar_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         ptx::smem_u32(tmem_slot)),
-                     "r"(kTmemCols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             ptx::smem_u32(tmem_slot)),
+                         "r"(kTmemCols));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             ptx::smem_u32(tmem_slot)),
+                         "r"(kTmemCols));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
     ptx::grid_dep_wait();
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync_all();  // barrier inits of both CTAs visible before any cross-CTA signal
+    } else {
+        __syncthreads();
+    }
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
         if (lane == 0) {
             int it = 0;  // global k-stage counter
-            for (int64_t w = blockIdx.x; w < n_work && !abort_flag; w += gridDim.x) {
+            for (int64_t w = unit; w < n_work && !abort_flag; w += n_units) {
                 const int64_t t  = w % tiles;
                 const int     sp = (int) (w / tiles);
-                const int m0 = (int) ((t % m_tiles) * kBM), n0 = (int) ((t / m_tiles) * kBN);
+                const int ma = (int) ((t % m_tiles) * Cf::kTileM) + (int) rank * 128;  // this CTA's A rows
+                const int nb = (int) ((t / m_tiles) * kBN) + (int) rank * Cf::kRowsB;  // this CTA's B rows
                 const int kt1 = min(k_tiles, (sp + 1) * g.kps);
                 for (int kt = sp * g.kps; kt < kt1; kt++, it++) {
-                    const int s = it % kStages;
-                    if (it >= kStages && !ptx::mbar_wait(&empty[s], ((it / kStages) - 1) & 1)) {
+                    const int s = it % Cf::kStages;
+                    if (it >= Cf::kStages && !ptx::mbar_wait(&empty[s], ((it / Cf::kStages) - 1) & 1)) {
                         flag_timeout(g.err);
                         abort_flag = 1;
                         break;
                     }
-                    uint8_t * st = ring + (size_t) s * kStageBytes;
-                    ptx::mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d(st, &tmA, kt * kBK, m0, &full[s]);
-                    tma_load_2d(st + kATile, &tmB, kt * kBK, n0, &full[s]);
+                    uint8_t * st = ring + (size_t) s * Cf::kStage;
+                    if constexpr (PAIR) {
+                        const uint32_t fb = mapa_shared(ptx::smem_u32(&full[s]), 0);
+                        if (leader) {
+                            ptx::mbar_arrive_expect_tx(&full[s], Cf::kTx);
+                        }
+                        tma_load_2d_pair(st, &tmA, kt * kBK, ma, fb);
+                        tma_load_2d_pair(st + Cf::kATile, &tmB, kt * kBK, nb, fb);
+                    } else {
+                        ptx::mbar_arrive_expect_tx(&full[s], Cf::kTx);
+                        tma_load_2d(st, &tmA, kt * kBK, ma, &full[s]);
+                        tma_load_2d(st + Cf::kATile, &tmB, kt * kBK, nb, &full[s]);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            constexpr uint32_t idesc = idesc_kind_f16(kBM, kBN, F16);
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_kind_f16(Cf::kTileM, kBN, F16);
             int                it    = 0;
             int                tile  = 0;
-            for (int64_t w = blockIdx.x; w < n_work && !abort_flag; w += gridDim.x, tile++) {
+            for (int64_t w = unit; w < n_work && !abort_flag; w += n_units, tile++) {
                 const int acc = tile & 1;
-                if (tile >= 2 && !ptx::mbar_wait(&tmem_empty[acc], ((tile >> 1) - 1) & 1)) {
+                if (tile >= 2 && !mbar_wait_cluster(&tmem_empty[acc], ((tile >> 1) - 1) & 1)) {
                     flag_timeout(g.err);
                     abort_flag = 1;
                     break;
@@ -157,23 +199,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int      kt0    = (int) (w / tiles) * g.kps;
                 const int      kt1    = min(k_tiles, kt0 + g.kps);
                 for (int kt = kt0; kt < kt1; kt++, it++) {
-                    const int s = it % kStages;
-                    if (!ptx::mbar_wait(&full[s], (it / kStages) & 1)) {
+                    const int s = it % Cf::kStages;
+                    if (!ptx::mbar_wait(&full[s], (it / Cf::kStages) & 1)) {
                         flag_timeout(g.err);
                         abort_flag = 1;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = ptx::smem_u32(ring + (size_t) s * kStageBytes);
-                    const uint32_t b0 = a0 + kATile;
+                    const uint32_t a0 = ptx::smem_u32(ring + (size_t) s * Cf::kStage);
+                    const uint32_t b0 = a0 + Cf::kATile;
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; kk++) {
-                        umma_f16kind(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                                  (kt != kt0 || kk != 0) ? 1u : 0u);
+                        const uint32_t accumulate = (kt != kt0 || kk != 0) ? 1u : 0u;
+                        if constexpr (PAIR) {
+                            umma_f16kind_pair(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
+                                              idesc, accumulate);
+                        } else {
+                            umma_f16kind(tmem_d, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                                         accumulate);
+                        }
                     }
-                    umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                    // frees the stage (in both CTAs) once these MMAs have read it
+                    if constexpr (PAIR) {
+                        umma_commit_pair(&empty[s]);
+                    } else {
+                        umma_commit(&empty[s]);
+                    }
                 }
-                umma_commit(&tmem_full[acc]);  // accumulator complete
+                if constexpr (PAIR) {  // accumulator complete
+                    umma_commit_pair(&tmem_full[acc]);
+                } else {
+                    umma_commit(&tmem_full[acc]);
+                }
             }
         }
     } else {
@@ -181,7 +238,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int q    = warp & 3;
         const int row_in_tile = q * 32 + lane;
         int       tile = 0;
-        for (int64_t w = blockIdx.x; w < n_work; w += gridDim.x, tile++) {
+        for (int64_t w = unit; w < n_work; w += n_units, tile++) {
             const int acc = tile & 1;
             if (!ptx::mbar_wait(&tmem_full[acc], (tile >> 1) & 1)) {
                 if (lane == 0) {
@@ -192,7 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_after();
             const int64_t t  = w % tiles;
-            const int64_t m  = (t % m_tiles) * kBM + row_in_tile;
+            const int64_t m  = (t % m_tiles) * Cf::kTileM + (int64_t) rank * 128 + row_in_tile;
             const int64_t n0 = (t / m_tiles) * kBN;
             const bool    part = g.splits > 1;  // raw partial of split w / tiles
             float *       pdst = part ? g.ws + ((w / tiles) * g.M + m) * g.N : nullptr;
@@ -265,16 +322,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                ptx::mbar_arrive(&tmem_empty[acc]);
+                if (leader) {
+                    ptx::mbar_arrive(&tmem_empty[acc]);
+                } else {  // the pair's accumulators are handed back to the leader's MMA thread
+                    mbar_arrive_cluster(mapa_shared(ptx::smem_u32(&tmem_empty[acc]), 0));
+                }
             }
         }
     }
     ptx::grid_dep_launch();
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) {
+        cluster_sync_all();  // no MMA, load or arrival of either CTA still targets the other
+    } else {
+        __syncthreads();
+    }
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+        } else {
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols));
+        }
     }
 }
 
@@ -333,7 +402,7 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs g) {
 // Split-K factor for an M x N x K GEMM: only when the output tiles leave most SMs idle; every
 // split keeps at least 4 k-tiles (256 of K) so its pipeline fill stays amortised.
 static int choose_splits(int64_t M, int64_t N, int64_t K, int * kps) {
-    const int64_t tiles   = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
+    const int64_t tiles   = ((M + 127) / 128) * ((N + kBN - 1) / kBN);
     const int     k_tiles = (int) (K / kBK);
     const int     sms     = num_sms();
     *kps                  = k_tiles;
@@ -356,9 +425,52 @@ static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K
     return make_map_2d(m, base, f16, K, rows, ld, kBK, box_rows);
 }
 
+// Clusters of two CTAs that can be resident at once for the pair kernel (0: pairs off). Cached
+// per operand type; ACB_GEMM_PAIR=0 in the environment turns the pair kernel off.
+static int pair_clusters(bool f16) {
+    static int n[2] = { -1, -1 };
+    int &      c    = n[f16 ? 1 : 0];
+    if (c < 0) {
+        c                 = 0;
+        const char * env = getenv("ACB_GEMM_PAIR");
+        if (env && env[0] == '0') {
+            return c;
+        }
+        void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
+            f16 ? gemm_tc_kernel<true, true> : gemm_tc_kernel<false, true>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) GemmCfg<true>::kSmem) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return c;
+        }
+        cudaLaunchConfig_t  cfg = {};
+        cudaLaunchAttribute a;
+        a.id                 = cudaLaunchAttributeClusterDimension;
+        a.val.clusterDim.x   = 2;
+        a.val.clusterDim.y   = 1;
+        a.val.clusterDim.z   = 1;
+        cfg.gridDim          = dim3(2 * (unsigned) num_sms());
+        cfg.blockDim         = dim3(kGemmThreads);
+        cfg.dynamicSmemBytes = GemmCfg<true>::kSmem;
+        cfg.attrs            = &a;
+        cfg.numAttrs         = 1;
+        int k                = 0;
+        if (cudaOccupancyMaxActiveClusters(&k, kern, &cfg) == cudaSuccess && k > 0) {
+            c = k;
+        } else {
+            cudaGetLastError();
+        }
+    }
+    return c;
+}
+
 }  // namespace acb
 
 using namespace acb;
+
+extern "C" int acb_gemm_pair_clusters(int f16) {
+    return pair_clusters(f16 != 0);
+}
 
 extern "C" size_t acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0) {
@@ -414,35 +526,56 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
             g.ws     = reinterpret_cast<float *>(workspace);
         }
     }
-    const bool  f16 = (flags & ACB_FLAG_F16) != 0;
+    const bool f16 = (flags & ACB_FLAG_F16) != 0;
+    // CTA pairs when the single-CTA tiling needs no split (enough 256x256 tiles to fill the GPU)
+    const int  clusters = g.splits == 1 && M > 128 ? pair_clusters(f16) : 0;
+    const bool pair     = clusters > 0;
     CUtensorMap ta, tb;
-    if (!make_map(&ta, A, M, K, lda, kBM, f16) || !make_map(&tb, B, N, K, ldb, kBN, f16)) {
+    if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, N, K, ldb, pair ? 128 : kBN, f16)) {
         return ACB_ERR_CUDA;
     }
-    const int64_t work = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * g.splits;
-    const int     grid = (int) (work < num_sms() ? work : num_sms());
-    const size_t  smem = (size_t) kStages * kStageBytes + 1024 + 256;
-    void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
-        f16 ? gemm_tc_kernel<true> : gemm_tc_kernel<false>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim            = dim3((unsigned) grid);
     cfg.blockDim           = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes   = smem;
     cfg.stream             = (cudaStream_t) stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs                                          = (flags & ACB_FLAG_PDL) ? attr : nullptr;
-    cfg.numAttrs                                       = (flags & ACB_FLAG_PDL) ? 1 : 0;
-    cudaError_t e                                      = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+    cudaLaunchAttribute attr[2];
+    int                 na = 0;
+    if (pair) {
+        attr[na].id               = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 2;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cudaLaunchAttribute & pdl = attr[na];
+    pdl.id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl.val.programmaticStreamSerializationAllowed = 1;
+    if (flags & ACB_FLAG_PDL) {
+        na++;
+    }
+    cfg.attrs    = na ? attr : nullptr;
+    cfg.numAttrs = na;
+    cudaError_t e;
+    if (pair) {
+        const int64_t work = ((M + 255) / 256) * ((N + kBN - 1) / kBN);
+        cfg.gridDim          = dim3((unsigned) (2 * (work < clusters ? work : clusters)));
+        cfg.dynamicSmemBytes = GemmCfg<true>::kSmem;
+        e = cudaLaunchKernelEx(&cfg, f16 ? gemm_tc_kernel<true, true> : gemm_tc_kernel<false, true>, ta, tb, g);
+    } else {
+        const int64_t work = ((M + 127) / 128) * ((N + kBN - 1) / kBN) * g.splits;
+        void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
+            f16 ? gemm_tc_kernel<true, false> : gemm_tc_kernel<false, false>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) GemmCfg<false>::kSmem);
+        cfg.gridDim          = dim3((unsigned) (work < num_sms() ? work : num_sms()));
+        cfg.dynamicSmemBytes = GemmCfg<false>::kSmem;
+        e                    = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+    }
     if (e == cudaSuccess && g.splits > 1) {
         // the reduction always waits on the GEMM through griddepcontrol.wait
         const int64_t n_thr = M * (N / 4);
         cfg.gridDim         = dim3((unsigned) ((n_thr + 255) / 256));
         cfg.blockDim        = dim3(256);
         cfg.dynamicSmemBytes = 0;
-        cfg.attrs           = attr;
+        cfg.attrs           = &pdl;
         cfg.numAttrs        = 1;
         e                   = cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, g);
     }

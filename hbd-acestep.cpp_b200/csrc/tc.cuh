@@ -92,6 +92,78 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) ---------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// every thread of every CTA in the cluster (non-aligned form: callable after divergent roles);
+// orders shared-memory work at cluster scope
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// arrive (release, cluster scope) on an mbarrier given by its shared::cluster address
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// bounded wait with cluster-scope acquire (the barrier receives arrivals from the peer CTA)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t * bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+    for (uint32_t i = 0; i < limit; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(ptx::smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) {
+            return true;
+        }
+    }
+    return false;
+}
+
+// Tile load of a CTA pair: the data lands in this CTA's shared memory, the transaction bytes are
+// counted on the mbarrier at `bar_cluster` (the pair leader's barrier). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void * dst, const CUtensorMap * map, int x, int y,
+                                                 uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+        "%3}], [%4];" ::"r"(ptx::smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+
+// Pair MMA issued by the leader: D (each CTA's TMEM: its 128 rows) += A (each CTA's 128 rows)
+// x B (N/2 rows from each CTA); descriptors name the same offsets in both CTAs' shared memory.
+__device__ __forceinline__ void umma_f16kind_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                                  uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// completion of the leader's prior pair MMAs signalled on the mbarrier at this offset in both CTAs
+__device__ __forceinline__ void umma_commit_pair(uint64_t * bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            ptx::smem_u32(bar)),
+        "h"((uint16_t) 3)
+        : "memory");
+}
+
 // ---- host: tensor maps through the driver entry point (no libcuda link) ----------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,

@@ -210,6 +210,12 @@ ACB_API acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, in
  * bytes needed at these sizes (0: no split is used); a smaller or NULL workspace runs unsplit.
  * Calls sharing one workspace must not overlap. */
 ACB_API size_t     acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* Unsplit GEMMs with M > 128 run on CTA pairs (clusters of two, tcgen05 cta_group::2, 256 x 256
+ * output tiles, each CTA loading half of the B tile). Returns how many pairs fit on this device
+ * at once (0: the pair kernel is off, e.g. ACB_GEMM_PAIR=0 in the environment). No reference
+ * counterpart: a query of this library's tiling. */
+ACB_API int        acb_gemm_pair_clusters(int f16);
 ACB_API acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
                                int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
                                int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,

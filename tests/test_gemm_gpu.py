@@ -133,3 +133,38 @@ def test_gemm_exact_split_products(cuda, M, N, K):
     C = acb.gemm_bf16(A, B, workspace=ws).double().cpu().numpy()
     ref = xd.astype(np.float64) @ wd.astype(np.float64).T
     assert max_rel(C, ref) <= 2e-6, max_rel(C, ref)
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_gemm_cta_pairs(cuda, f16):
+    """Unsplit GEMMs with M > 128 run on CTA pairs (256 x 256 tiles over two SMs). Ragged M and N
+    leave the second CTA of the last pair tiles partly (rows 2432..2499) or wholly out of range,
+    and 80 tiles over the resident pairs make some pairs reuse both TMEM accumulators. Every
+    epilogue, against the fp32 reference; repeat runs are bit-identical."""
+    import torch
+    assert acb.gemm_pair_clusters(f16) > 0, "the CTA-pair kernel should be available on B200"
+    dt = torch.float16 if f16 else torch.bfloat16
+    g = torch.Generator(device=cuda).manual_seed(11 + f16)
+    S, T, K, N = 4, 625, 1024, 2000
+    M = S * T
+    A = torch.randn(M, K, device=cuda, generator=g).to(dt)
+    B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(dt)
+    bias = torch.randn(N, device=cuda, generator=g)
+    res = torch.randn(M, N, device=cuda, generator=g)
+    gate = torch.randn(S, N, device=cuda, generator=g)
+    base = ref_mm(A, B)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    C1 = acb.gemm_bf16(A, B, err=err)
+    C2 = acb.gemm_bf16(A, B, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert max_rel(C1.cpu().numpy(), base.cpu().numpy()) <= 1e-5
+    assert torch.equal(C1, C2)
+    out = res.clone()
+    acb.gemm_bf16(A, B, out=out, bias=bias, res=out, gate=gate, rows_per_sample=T)
+    want = res + (base + bias) * gate.repeat_interleave(T, dim=0)
+    assert max_rel((out - res).cpu().numpy(), (want - res).cpu().numpy()) <= 1e-5
+    Cb = acb.gemm_bf16(A, B, out_dtype=dt)
+    d = (Cb.float() - base).abs()
+    ulp = 2.0 ** -10 if f16 else 2.0 ** -8
+    assert (d <= base.abs() * ulp + 2e-5 * base.abs().max()).all()
