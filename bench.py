@@ -575,7 +575,18 @@ def run_gemm_shapes(dev, reps=20, which=None):
             us = e0.elapsed_time(e1) / reps * 1e3
             tf = 2.0 * M * N * Kp / (us * 1e-6) / 1e12
             res[mode] = {"us": round(us, 1), "TFLOP/s": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 3)}
-            del A, B, C
+            # the same product through cuBLAS (torch.matmul, 16-bit output), for comparison only
+            Cl = torch.empty(M, N, device=dev, dtype=dt)
+            for _ in range(3):
+                torch.matmul(A, B.T, out=Cl)
+            e0.record()
+            for _ in range(reps):
+                torch.matmul(A, B.T, out=Cl)
+            e1.record()
+            torch.cuda.synchronize()
+            us_l = e0.elapsed_time(e1) / reps * 1e3
+            res[mode]["cublas_TFLOP/s"] = round(2.0 * M * N * Kp / (us_l * 1e-6) / 1e12, 1)
+            del A, B, C, Cl
         out["shapes"][name] = res
     return out
 

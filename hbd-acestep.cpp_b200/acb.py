@@ -115,6 +115,8 @@ def lib():
             "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
             "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
             "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
+            "acb_norm_quant": (I, [P, I64, I64, I64, P, F, P, P, I64, I64, I, I, P, I, I64, I64, P]),
+            "acb_qk_norm_rope_planes": (I, [P, I, I64, P, I64, I64, I64, I, I, P, F, P, P, I, P, P]),
             "acb_attn_prefill_split": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I,
                                            I, I, F, I, I64, I64, I64, P]),
             "acb_qwen3_free": (None, [P]),
@@ -547,6 +549,36 @@ def act_quant_ex(x, K, vec_type, layout, up_offset=0, out=None, lo_offset=0, str
             lo_offset = M * width
     _check("acb_act_quant_ex", lib().acb_act_quant_ex(_ptr(x), x.stride(0), up_offset, M, K, vec_type, layout,
                                                       _ptr(out), dtype_id(out), width, lo_offset, _stream(stream)))
+    return out
+
+
+def norm_quant(x, K, w, eps, vec_type, layout, scale=None, shift=None, rows_per_sample=None, vec_stride=0,
+               stream=None):
+    """acb_norm_quant over x [M, >=K] f32: RMSNorm (times w) [adaLN with scale/shift] then the
+    activation quantiser of act_quant_ex (layouts PLAIN, GEMM_A, PLANES)."""
+    import torch
+    M = x.shape[0]
+    dt = torch.bfloat16 if vec_type == BF16 else torch.float16
+    width = 3 * K if layout == LAYOUT_GEMM_A else K
+    out = torch.empty((2 * M if layout == LAYOUT_PLANES else M, width), dtype=dt, device=x.device)
+    lo_offset = M * width if layout == LAYOUT_PLANES else 0
+    rps = rows_per_sample if rows_per_sample is not None else M
+    _check("acb_norm_quant", lib().acb_norm_quant(_ptr(x), x.stride(0), M, K, _ptr(w), eps, _ptr(scale), _ptr(shift),
+                                                  vec_stride, rps, vec_type, layout, _ptr(out), dtype_id(out), width,
+                                                  lo_offset, _stream(stream)))
+    return out
+
+
+def qk_norm_rope_planes(src, n_heads, w, eps, pos=None, rope=None, err=None, stream=None):
+    """acb_qk_norm_rope_planes: src [T, >= n_heads*128] -> f16 planes [2T, n_heads*128] (hi rows
+    then lo rows)."""
+    import torch
+    T, W = src.shape[0], n_heads * 128
+    out = torch.empty((2 * T, W), dtype=torch.float16, device=src.device)
+    max_pos = rope.shape[0] if rope is not None else 0
+    _check("acb_qk_norm_rope_planes", lib().acb_qk_norm_rope_planes(
+        _ptr(src), dtype_id(src), src.stride(0), _ptr(out), W, T * W, T, n_heads, 128, _ptr(w), eps, _ptr(pos),
+        _ptr(rope), max_pos, _ptr(err), _stream(stream)))
     return out
 
 

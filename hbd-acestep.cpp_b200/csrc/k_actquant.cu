@@ -52,39 +52,10 @@ template <int OT, int LAYOUT>
 __device__ __forceinline__ void split_store(typename io<OT>::t * yr, const float * o, int64_t K, int64_t lo_off,
                                             bool vec_out);
 
-template <int VT, bool SWIGLU, int LAYOUT>
-__global__ void __launch_bounds__(kAqWarps * 32)
-    act_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t up_off, int64_t rows, int64_t K,
-                     void * __restrict__ y, int64_t ys, int64_t lo_off, bool vec_in, bool vec_out) {
-    const int     lane   = threadIdx.x & 31;
-    const int64_t chunks = (K + 255) / 256;
-    const int64_t item   = (int64_t) blockIdx.x * kAqWarps + (threadIdx.x >> 5);
-    if (item >= rows * chunks) {
-        return;
-    }
-    const int64_t r     = item / chunks;
-    const int64_t c0    = (item - r * chunks) * 256 + lane * 8;
-    const bool    valid = c0 < K;  // K is a multiple of 32: a lane is all in or all out
-    const float * xr    = x + r * xs + c0;
-    float         v[8];
-    if (valid) {
-        load8(xr, vec_in, v);
-        if (SWIGLU) {
-            float u[8];
-            load8(xr + up_off, vec_in, u);
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                v[e] = silu_times(v[e], u[e]);
-            }
-        }
-    } else {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            v[e] = 0.0f;
-        }
-    }
-
-    float o[8];
+// ggml's from_float of one lane's 8 consecutive values (v) to the dequantised operand values
+// (o): Q8_0 blocks of 32 are four consecutive lanes, a Q8_K block of 256 is the whole warp
+// (all 32 lanes must call it together); F16 / BF16 / F32 pass the values through.
+template <int VT> __device__ __forceinline__ void quant8(const float * v, int lane, float * o) {
     if (VT == ACB_TYPE_Q8_0) {
         float amax = 0.0f;
 #pragma unroll
@@ -145,6 +116,43 @@ __global__ void __launch_bounds__(kAqWarps * 32)
             o[e] = v[e];
         }
     }
+}
+
+
+template <int VT, bool SWIGLU, int LAYOUT>
+__global__ void __launch_bounds__(kAqWarps * 32)
+    act_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t up_off, int64_t rows, int64_t K,
+                     void * __restrict__ y, int64_t ys, int64_t lo_off, bool vec_in, bool vec_out) {
+    const int     lane   = threadIdx.x & 31;
+    const int64_t chunks = (K + 255) / 256;
+    const int64_t item   = (int64_t) blockIdx.x * kAqWarps + (threadIdx.x >> 5);
+    if (item >= rows * chunks) {
+        return;
+    }
+    const int64_t r     = item / chunks;
+    const int64_t c0    = (item - r * chunks) * 256 + lane * 8;
+    const bool    valid = c0 < K;  // K is a multiple of 32: a lane is all in or all out
+    const float * xr    = x + r * xs + c0;
+    float         v[8];
+    if (valid) {
+        load8(xr, vec_in, v);
+        if (SWIGLU) {
+            float u[8];
+            load8(xr + up_off, vec_in, u);
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                v[e] = silu_times(v[e], u[e]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            v[e] = 0.0f;
+        }
+    }
+
+    float o[8];
+    quant8<VT>(v, lane, o);
     if (!valid) {
         return;
     }
@@ -180,6 +188,90 @@ __device__ __forceinline__ void split_store(typename io<OT>::t * yr, const float
     } else {  // ACB_LAYOUT_PLANES: hi here, lo at lo_off elements further
         store8<OT>(yr, hi, vec_out);
         store8<OT>(yr + lo_off, lo, vec_out);
+    }
+}
+
+
+// RMSNorm (+ weight) [+ adaLN modulate] of a row followed by the quantisation above, in one pass:
+// ggml_rms_norm -> ggml_mul(w) [-> ggml_mul(1 + scale) -> ggml_add(shift)] and then the
+// from_float of the next ggml_mul_mat (src/dit-graph.h:150-157, 250-258; src/qwen3-enc.h:80-90),
+// with every product and sum rounded as those separate graph nodes round them. One warp per
+// row; lane l holds elements [256c + 8l, 256c + 8l + 8) of chunk c in registers. Without a
+// weight, the adaLN form skips the normalisation (as acb_adaln_modulate does).
+template <int VT, int LAYOUT, int NCH, bool ADALN>
+__global__ void __launch_bounds__(kAqWarps * 32)
+    norm_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t rows, int64_t K, const float * __restrict__ w,
+                      float eps, const float * __restrict__ scale, const float * __restrict__ shift, int64_t vs,
+                      int64_t rps, void * __restrict__ y, int64_t ys, int64_t lo_off, bool vec_in, bool vec_out) {
+    const int     lane = threadIdx.x & 31;
+    const int64_t r    = (int64_t) blockIdx.x * kAqWarps + (threadIdx.x >> 5);
+    if (r >= rows) {
+        return;
+    }
+    const float * xr = x + r * xs;
+    float         v[NCH][8];
+    double        ss = 0.0;
+#pragma unroll
+    for (int c = 0; c < NCH; c++) {
+        const int64_t c0 = (int64_t) c * 256 + lane * 8;
+        if (c0 < K) {
+            load8(xr + c0, vec_in, v[c]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                v[c][e] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            ss += (double) __fmul_rn(v[c][e], v[c][e]);
+        }
+    }
+    const bool do_norm = !ADALN || w != nullptr;
+    ss                 = warp_sum(ss);
+    const float   sc   = do_norm ? rms_scale(ss, (int) K, eps) : 1.0f;
+    const int64_t smp  = ADALN ? r / rps : 0;
+    constexpr int OT   = VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
+    using et           = typename io<OT>::t;
+#pragma unroll
+    for (int c = 0; c < NCH; c++) {
+        const int64_t c0    = (int64_t) c * 256 + lane * 8;
+        const bool    valid = c0 < K;
+        if (VT != ACB_TYPE_Q8_K && (int64_t) c * 256 >= K) {
+            break;  // warp-uniform: no lane of this chunk is in the row
+        }
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            f[e] = 0.0f;
+        }
+        if (valid) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                float t = v[c][e];
+                if (do_norm) {
+                    t = __fmul_rn(t, sc);
+                    if (w) {
+                        t = __fmul_rn(t, __ldg(w + c0 + e));
+                    }
+                }
+                if (ADALN) {
+                    t = __fadd_rn(__fmul_rn(t, __fadd_rn(__ldg(scale + smp * vs + c0 + e), 1.0f)),
+                                  __ldg(shift + smp * vs + c0 + e));
+                }
+                f[e] = t;
+            }
+        }
+        float o[8];
+        quant8<VT>(f, lane, o);
+        if (valid) {
+            et * yr = reinterpret_cast<et *>(y) + r * ys + c0;
+            if constexpr (LAYOUT == ACB_LAYOUT_PLAIN) {
+                store8<OT>(yr, o, vec_out);
+            } else {
+                split_store<OT, LAYOUT>(yr, o, K, lo_off, vec_out);
+            }
+        }
     }
 }
 
@@ -307,4 +399,111 @@ extern "C" acb_status acb_act_quant_ex(const float * x, int64_t x_stride, int64_
     }
     return launch_act_quant<false>(x, x_stride, 0, rows, K, vec_type, layout, y, y_type, y_stride, lo_offset,
                                    (cudaStream_t) stream);
+}
+
+namespace {
+
+template <int VT, int LAYOUT, bool ADALN>
+void launch_nq_nch(int nch, dim3 grid, cudaStream_t st, const float * x, int64_t xs, int64_t rows, int64_t K,
+                   const float * w, float eps, const float * scale, const float * shift, int64_t vs, int64_t rps,
+                   void * y, int64_t ys, int64_t lo_off, bool vin, bool vout) {
+#define ACB_NQ(N)                                                                                                  \
+    norm_quant_kernel<VT, LAYOUT, N, ADALN><<<grid, kAqWarps * 32, 0, st>>>(x, xs, rows, K, w, eps, scale, shift, \
+                                                                             vs, rps, y, ys, lo_off, vin, vout)
+    if (nch <= 4) {
+        ACB_NQ(4);
+    } else if (nch <= 8) {
+        ACB_NQ(8);
+    } else if (nch <= 12) {
+        ACB_NQ(12);
+    } else {
+        ACB_NQ(16);
+    }
+#undef ACB_NQ
+}
+
+template <int VT, bool ADALN>
+void launch_nq_layout(int layout, int nch, dim3 grid, cudaStream_t st, const float * x, int64_t xs, int64_t rows,
+                      int64_t K, const float * w, float eps, const float * scale, const float * shift, int64_t vs,
+                      int64_t rps, void * y, int64_t ys, int64_t lo_off, bool vin, bool vout) {
+    switch (layout) {
+        case ACB_LAYOUT_GEMM_A:
+            launch_nq_nch<VT, ACB_LAYOUT_GEMM_A, ADALN>(nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps,
+                                                        y, ys, lo_off, vin, vout);
+            break;
+        case ACB_LAYOUT_PLANES:
+            launch_nq_nch<VT, ACB_LAYOUT_PLANES, ADALN>(nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps,
+                                                        y, ys, lo_off, vin, vout);
+            break;
+        default:
+            launch_nq_nch<VT, ACB_LAYOUT_PLAIN, ADALN>(nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps,
+                                                       y, ys, lo_off, vin, vout);
+    }
+}
+
+template <bool ADALN>
+acb_status launch_norm_quant(int vec_type, int layout, const float * x, int64_t xs, int64_t rows, int64_t K,
+                             const float * w, float eps, const float * scale, const float * shift, int64_t vs,
+                             int64_t rps, void * y, int64_t ys, int64_t lo_off, cudaStream_t st) {
+    const bool vin = (xs % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    const bool vout =
+        (ys % 8 == 0) && (K % 8 == 0) && (lo_off % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
+    const int  nch = (int) ((K + 255) / 256);
+    const dim3 grid((unsigned) ((rows + kAqWarps - 1) / kAqWarps));
+#define ACB_NQV(V) \
+    launch_nq_layout<V, ADALN>(layout, nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps, y, ys, lo_off, vin, vout)
+    switch (vec_type) {
+        case ACB_TYPE_Q8_0:
+            ACB_NQV(ACB_TYPE_Q8_0);
+            break;
+        case ACB_TYPE_Q8_K:
+            ACB_NQV(ACB_TYPE_Q8_K);
+            break;
+        case ACB_TYPE_F16:
+            ACB_NQV(ACB_TYPE_F16);
+            break;
+        case ACB_TYPE_F32:
+            ACB_NQV(ACB_TYPE_F32);
+            break;
+        case ACB_TYPE_BF16:
+            ACB_NQV(ACB_TYPE_BF16);
+            break;
+        default:
+            return ACB_ERR_UNSUPPORTED;
+    }
+#undef ACB_NQV
+    return launch_status();
+}
+
+}  // namespace
+
+extern "C" acb_status acb_norm_quant(const float * x, int64_t x_stride, int64_t rows, int64_t K, const float * norm_w,
+                                     float eps, const float * scale, const float * shift, int64_t vec_stride,
+                                     int64_t rows_per_sample, int vec_type, int layout, void * y, int y_type,
+                                     int64_t y_stride, int64_t lo_offset, acb_stream_t stream) {
+    if (!x || !y || rows < 0 || K <= 0 || x_stride < K || y_stride < K || (!scale != !shift) || vec_stride < 0 ||
+        (scale && rows_per_sample <= 0)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (layout == ACB_LAYOUT_PLANES && lo_offset == 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int want_y = vec_type == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
+    if (y_type != want_y || K % 32 != 0 || K > 4096 || (vec_type == ACB_TYPE_Q8_K && K % 256 != 0) ||
+        layout == ACB_LAYOUT_GEMM_B || layout < 0 || layout > 3) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (layout == ACB_LAYOUT_GEMM_A && y_stride < 3 * K) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (rows == 0) {
+        return ACB_OK;
+    }
+    cudaStream_t st = (cudaStream_t) stream;
+    if (scale) {
+        return launch_norm_quant<true>(vec_type, layout, x, x_stride, rows, K, norm_w, eps, scale, shift, vec_stride,
+                                       rows_per_sample, y, y_stride, lo_offset, st);
+    }
+    return launch_norm_quant<false>(vec_type, layout, x, x_stride, rows, K, norm_w, eps, nullptr, nullptr, 0, 1, y,
+                                    y_stride, lo_offset, st);
 }

@@ -235,12 +235,14 @@ static acb_status dispatch_row_norm(int ti, int to, const void * x, int64_t xs, 
 // ---- per-head q/k RMSNorm + NeoX RoPE ------------------------------------------------------
 // One warp per (token, head). Lane l owns E = D/64 consecutive elements of the first half
 // starting at l*E and the matching elements of the second half, so each NeoX pair (i, i+D/2)
-// lives in one lane.
-template <int TI, int TO, int E>
+// lives in one lane. SPLIT (f16 output): the result is also written as exact hi/lo planes,
+// hi = f16(v) at dst and lo = f16(v - hi) lo_off elements further (the operand planes of the
+// split-precision attention), instead of one rounded copy.
+template <int TI, int TO, int E, bool SPLIT = false>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const void * __restrict__ src, int64_t sts, void * __restrict__ dst, int64_t dts, int64_t dhs, int64_t dps,
     int64_t n_tok, int n_heads, const float * __restrict__ w, float eps, const int32_t * __restrict__ pos,
-    const float * __restrict__ rope, int max_pos, int * __restrict__ err) {
+    const float * __restrict__ rope, int max_pos, int * __restrict__ err, int64_t lo_off = 0) {
     using ei              = typename io<TI>::t;
     using eo              = typename io<TO>::t;
     constexpr int D       = 64 * E;
@@ -302,6 +304,10 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     for (int e = 0; e < E; e++) {
         d[e]        = io<TO>::from_f(a[e]);
         d[HALF + e] = io<TO>::from_f(b[e]);
+        if constexpr (SPLIT) {
+            d[lo_off + e]        = io<TO>::from_f(__fsub_rn(a[e], io<TO>::to_f(d[e])));
+            d[lo_off + HALF + e] = io<TO>::from_f(__fsub_rn(b[e], io<TO>::to_f(d[HALF + e])));
+        }
     }
 }
 
@@ -395,4 +401,36 @@ extern "C" acb_status acb_qk_norm_rope(const void * src, int src_type, int64_t s
     ACB_QK(ACB_TYPE_F16, ACB_TYPE_F16)
 #undef ACB_QK
     return ACB_ERR_UNSUPPORTED;
+}
+
+extern "C" acb_status acb_qk_norm_rope_planes(const void * src, int src_type, int64_t src_tok_stride, uint16_t * dst,
+                                              int64_t dst_tok_stride, int64_t lo_offset, int64_t n_tok, int n_heads,
+                                              int head_dim, const float * norm_w, float eps, const int32_t * pos,
+                                              const float * rope_table, int max_pos, int * err_flag,
+                                              acb_stream_t stream) {
+    if (!src || !dst || n_tok < 0 || n_heads <= 0 || lo_offset <= 0 || dst_tok_stride < (int64_t) n_heads * head_dim) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (rope_table && (!pos || max_pos <= 0)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (head_dim != 128 || (src_type != ACB_TYPE_F32 && src_type != ACB_TYPE_F16)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (n_tok == 0) {
+        return ACB_OK;
+    }
+    const int64_t items = n_tok * n_heads;
+    const dim3    grid((unsigned) ((items + 7) / 8));
+    cudaStream_t  st = (cudaStream_t) stream;
+    if (src_type == ACB_TYPE_F32) {
+        qk_norm_rope_kernel<ACB_TYPE_F32, ACB_TYPE_F16, 2, true><<<grid, 256, 0, st>>>(
+            src, src_tok_stride, dst, dst_tok_stride, head_dim, 0, n_tok, n_heads, norm_w, eps, pos, rope_table,
+            max_pos, err_flag, lo_offset);
+    } else {
+        qk_norm_rope_kernel<ACB_TYPE_F16, ACB_TYPE_F16, 2, true><<<grid, 256, 0, st>>>(
+            src, src_tok_stride, dst, dst_tok_stride, head_dim, 0, n_tok, n_heads, norm_w, eps, pos, rope_table,
+            max_pos, err_flag, lo_offset);
+    }
+    return launch_status();
 }

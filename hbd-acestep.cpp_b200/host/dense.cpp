@@ -64,11 +64,19 @@ acb_status dense_build(DenseLinear & L, const std::vector<DevTensor *> & parts, 
 acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int64_t xs, int64_t up_off, int M,
                          void * C, int c_type, int64_t ldc, const float * bias, const float * res, int64_t ldr,
                          const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
-                         cudaStream_t st) {
+                         cudaStream_t st, const NormSpec * norm) {
     const bool    three  = exact && L.split;
     const int64_t Kp     = three ? 3 * (int64_t) L.K : L.K;
     const int     layout = three ? ACB_LAYOUT_GEMM_A : ACB_LAYOUT_PLAIN;
-    ACB_TRY(acb_act_quant_ex(x, xs, up_off, M, L.K, L.vec, layout, s.xq, L.act_type(), Kp, 0, (acb_stream_t) st));
+    if (norm) {
+        if (up_off != 0) {
+            return ACB_ERR_INVALID_ARG;
+        }
+        ACB_TRY(acb_norm_quant(x, xs, M, L.K, norm->w, norm->eps, norm->scale, norm->shift, norm->vec_stride,
+                               norm->rows_per_sample, L.vec, layout, s.xq, L.act_type(), Kp, 0, (acb_stream_t) st));
+    } else {
+        ACB_TRY(acb_act_quant_ex(x, xs, up_off, M, L.K, L.vec, layout, s.xq, L.act_type(), Kp, 0, (acb_stream_t) st));
+    }
     return acb_gemm_tc(s.xq, Kp, L.w, L.ldw, M, L.N, Kp, C, c_type, ldc, bias, res, ldr, gate, gate_stride,
                        rows_per_sample, ACB_FLAG_PDL | L.op, s.ws, s.ws_bytes, s.err, (acb_stream_t) st);
 }

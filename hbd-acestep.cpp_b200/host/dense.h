@@ -51,11 +51,23 @@ struct DenseScratch {
     int *   err      = nullptr;
 };
 
+// Row normalisation applied to x inside the activation producer (acb_norm_quant): RMSNorm times
+// w, then, with scale/shift, the adaLN modulation n * (1 + scale) + shift (one vector pair every
+// rows_per_sample rows, vec_stride apart).
+struct NormSpec {
+    const float * w               = nullptr;
+    float         eps             = 0.0f;
+    const float * scale           = nullptr;
+    const float * shift           = nullptr;
+    int64_t       vec_stride      = 0;
+    int64_t       rows_per_sample = 1;
+};
+
 // C[M][N] = epi(x . W^T): x f32 [M][xs] (with up_off > 0: silu(x) * x[up_off + .], the SwiGLU
 // input of a down projection); bias f32 [N] optional; res/gate as acb_gemm_tc.
 acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int64_t xs, int64_t up_off, int M,
                          void * C, int c_type, int64_t ldc, const float * bias, const float * res, int64_t ldr,
                          const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
-                         cudaStream_t st);
+                         cudaStream_t st, const NormSpec * norm = nullptr);
 
 }  // namespace acb

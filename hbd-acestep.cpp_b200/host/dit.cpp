@@ -261,7 +261,6 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     const DenseScratch sc    = scratch();
     int *              e     = err.as<int>();
     float *            hp    = h.as<float>();
-    float *            xp    = xn.as<float>();
     const float *      a     = ada.as<float>() + (size_t) l * 6 * H;
     const float *shift_sa = a, *scale_sa = a + H, *gate_sa = a + 2 * H;
     const float *shift_ff = a + 3 * H, *scale_ff = a + 4 * H, *gate_ff = a + 5 * H;
@@ -269,32 +268,35 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     const bool swa  = (l % 2 == 0) && c.sliding_window > 0 && S > c.sliding_window;
     const int  mask = swa ? 2 : 0;
 
-    // self-attention
-    ACB_TRY(acb_adaln_modulate(hp, ACB_TYPE_F32, (const float *) L.sa_norm->data, eps, scale_sa, shift_sa, 0, xp,
-                               ACB_TYPE_F32, 1, R, H, as));
+    // self-attention: adaLN (norm1, shift/scale_msa) inside the qkv projection's activation producer
+    NormSpec ns_sa;
+    ns_sa.w               = (const float *) L.sa_norm->data;
+    ns_sa.eps             = eps;
+    ns_sa.scale           = scale_sa;
+    ns_sa.shift           = shift_sa;
+    ns_sa.rows_per_sample = R;
     if (exact) {
         float * q32 = qkv32.as<float>();
-        ACB_TRY(dense_forward(L.sa_qkv, true, xp, H, 0, R, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0, 0,
-                              sc, s));
-        ACB_TRY(acb_qk_norm_rope(q32, ACB_TYPE_F32, NQKV, q32, ACB_TYPE_F32, NQKV, D, 0, R, Nh, D,
-                                 (const float *) L.sa_q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
-                                 as));
-        ACB_TRY(acb_qk_norm_rope(q32 + QD, ACB_TYPE_F32, NQKV, q32 + QD, ACB_TYPE_F32, NQKV, D, 0, R, Nkv, D,
-                                 (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
-                                 as));
-        // hi/lo planes of Q||K, and V transposed into hi/lo planes, for the tensor-core attention
+        ACB_TRY(dense_forward(L.sa_qkv, true, hp, H, 0, R, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0, 0,
+                              sc, s, &ns_sa));
+        // q/k RMSNorm + RoPE straight into hi/lo planes of Q||K, and V transposed into hi/lo
+        // planes, for the tensor-core attention
         const int64_t W  = QD + KD;
         const int64_t lo = (int64_t) R * W;
         uint16_t *    hi = planes.as<uint16_t>();
         const int64_t vl = (int64_t) Ng * KD * s_ld;
-        ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, R, W, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, W, lo, as));
+        ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, R, Nh, D, (const float *) L.sa_q_norm->data,
+                                        eps, pos.as<int32_t>(), rope.as<float>(), S, e, as));
+        ACB_TRY(acb_qk_norm_rope_planes(q32 + QD, ACB_TYPE_F32, NQKV, hi + QD, W, lo, R, Nkv, D,
+                                        (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S,
+                                        e, as));
         ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, vl, as));
         ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, Ng, S, S, Nh, Nkv, D, mask,
                             c.sliding_window, 0, scale, kPdl, lo, lo, vl, e, as));
     } else {
         uint16_t * q16p = qkv16.as<uint16_t>();
-        ACB_TRY(dense_forward(L.sa_qkv, false, xp, H, 0, R, q16p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
-                              0, sc, s));
+        ACB_TRY(dense_forward(L.sa_qkv, false, hp, H, 0, R, q16p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
+                              0, sc, s, &ns_sa));
         ACB_TRY(acb_qk_norm_rope(q16p, ACB_TYPE_F16, NQKV, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
                                  (const float *) L.sa_q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
                                  as));
@@ -308,33 +310,38 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ACB_TRY(dense_forward(L.sa_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0, R,
                           sc, s));
 
-    // cross-attention over the cached condition K/V
-    ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.ca_norm->data, xp, ACB_TYPE_F32, H, R, H, eps, as));
+    // cross-attention over the cached condition K/V; norm2 inside the q projection's producer
+    NormSpec ns_ca;
+    ns_ca.w   = (const float *) L.ca_norm->data;
+    ns_ca.eps = eps;
     float * cq = qkv32.as<float>();
-    ACB_TRY(dense_forward(L.ca_q, exact, xp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc, s));
-    ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, cq, ACB_TYPE_F32, QD, D, 0, R, Nh, D,
-                             (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
+    ACB_TRY(dense_forward(L.ca_q, exact, hp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc, s,
+                          &ns_ca));
     const uint16_t * k_hi  = kvcache.as<uint16_t>() + (size_t) l * kv_layer_elems;
     const uint16_t * vt_hi = k_hi + 2 * k_plane;
     if (exact) {
         const int64_t lo = (int64_t) R * QD;
         uint16_t *    qh = planes.as<uint16_t>();
-        ACB_TRY(acb_act_quant_ex(cq, QD, 0, R, QD, ACB_TYPE_F16, ACB_LAYOUT_PLANES, qh, ACB_TYPE_F16, QD, lo, as));
+        ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, D, (const float *) L.ca_q_norm->data,
+                                        eps, nullptr, nullptr, 0, e, as));
         ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
                             0, scale, kPdl, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
     } else {
-        ACB_TRY(acb_act_quant(cq, QD, R, QD, ACB_TYPE_F16, q16.p, ACB_TYPE_F16, QD, as));
+        ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
+                                 (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
         ACB_TRY(acb_attn_tc(q16.p, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0,
                             0, 0, scale, kPdl, 0, 0, 0, e, as));
     }
     ACB_TRY(dense_forward(L.ca_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
                           sc, s));
 
-    // FFN
-    ACB_TRY(acb_adaln_modulate(hp, ACB_TYPE_F32, (const float *) L.mlp_norm->data, eps, scale_ff, shift_ff, 0, xp,
-                               ACB_TYPE_F32, 1, R, H, as));
-    ACB_TRY(dense_forward(L.gu, exact, xp, H, 0, R, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0, sc,
-                          s));
+    // FFN: adaLN (norm3, shift/scale_mlp) inside the gate/up projection's producer
+    NormSpec ns_ff = ns_sa;
+    ns_ff.w        = (const float *) L.mlp_norm->data;
+    ns_ff.scale    = scale_ff;
+    ns_ff.shift    = shift_ff;
+    ACB_TRY(dense_forward(L.gu, exact, hp, H, 0, R, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0, sc,
+                          s, &ns_ff));
     return dense_forward(L.down, exact, gu.as<float>(), 2 * F, F, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_ff, 0, R,
                          sc, s);
 }
@@ -343,7 +350,6 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
 
 acb_status acb_dit::evaluate(int n_layers_run, cudaStream_t s) {
     const int          H = c.hidden_size, R = Ng * S, KP = c.in_channels * c.patch_size;
-    const acb_stream_t as = (acb_stream_t) s;
     const DenseScratch sc = scratch();
     ACB_TRY(timestep(s));
     ACB_TRY(dense_forward(proj_in, exact, input.as<float>(), KP, 0, R, h.p, ACB_TYPE_F32, H,
@@ -353,11 +359,15 @@ acb_status acb_dit::evaluate(int n_layers_run, cudaStream_t s) {
         ACB_TRY(layer(l, s));
     }
     const float * o = out_ss.as<float>();
-    ACB_TRY(acb_adaln_modulate(h.p, ACB_TYPE_F32, (const float *) norm_out->data, c.rms_norm_eps, o + H, o, 0, xn.p,
-                               ACB_TYPE_F32, 1, R, H, as));
+    NormSpec      ns;
+    ns.w               = (const float *) norm_out->data;
+    ns.eps             = c.rms_norm_eps;
+    ns.scale           = o + H;
+    ns.shift           = o;
+    ns.rows_per_sample = R;
     const int NO = c.out_channels * c.patch_size;
-    return dense_forward(proj_out, exact, xn.as<float>(), H, 0, R, vel.p, ACB_TYPE_F32, NO, proj_out_b.as<float>(),
-                         nullptr, 0, nullptr, 0, 0, sc, s);
+    return dense_forward(proj_out, exact, h.as<float>(), H, 0, R, vel.p, ACB_TYPE_F32, NO, proj_out_b.as<float>(),
+                         nullptr, 0, nullptr, 0, 0, sc, s, &ns);
 }
 
 // ---- loading (dit_ggml_load, src/dit.h:256-420) -----------------------------------------------------

@@ -156,36 +156,35 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
     const DenseScratch sc    = scratch();
     int *              e     = err.as<int>();
     float *            hp    = h.as<float>();
-    float *            xp    = xn.as<float>();
     const int          mask  = c.is_causal ? 1 : 0;
     for (int l = l0; l < l1; l++) {
         const EncLayer & L = layers[(size_t) l];
-        ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.attn_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
-                             as));
+        // input_layernorm inside the qkv projection's activation producer
+        NormSpec ns_in;
+        ns_in.w   = (const float *) L.attn_norm->data;
+        ns_in.eps = eps;
         if (exact) {
             float * q32 = qkv32.as<float>();
-            ACB_TRY(dense_forward(L.qkv, true, xp, H, 0, S, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0,
-                                  0, sc, s));
-            // q/k norm + rope in place (each warp reads its whole head before writing it)
-            ACB_TRY(acb_qk_norm_rope(q32, ACB_TYPE_F32, NQKV, q32, ACB_TYPE_F32, NQKV, D, 0, S, Nh, D,
-                                     (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
-                                     as));
-            ACB_TRY(acb_qk_norm_rope(q32 + QD, ACB_TYPE_F32, NQKV, q32 + QD, ACB_TYPE_F32, NQKV, D, 0, S, Nkv, D,
-                                     (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
-                                     as));
-            // hi/lo planes of Q||K and of V^T for the tensor-core attention
+            ACB_TRY(dense_forward(L.qkv, true, hp, H, 0, S, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0,
+                                  0, sc, s, &ns_in));
+            // q/k norm + rope straight into hi/lo planes of Q||K, and V^T planes, for the
+            // tensor-core attention
             const int64_t W  = QD + KD;
             const int64_t lo = (int64_t) cap * W;
             const int64_t vl = (int64_t) KD * s_ld;
             uint16_t *    hi = planes.as<uint16_t>();
-            ACB_TRY(acb_act_quant_ex(q32, NQKV, 0, S, W, ACB_TYPE_F16, ACB_LAYOUT_PLANES, hi, ACB_TYPE_F16, W, lo, as));
+            ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, S, Nh, D, (const float *) L.q_norm->data,
+                                            eps, pos.as<int32_t>(), rope.as<float>(), cap, e, as));
+            ACB_TRY(acb_qk_norm_rope_planes(q32 + QD, ACB_TYPE_F32, NQKV, hi + QD, W, lo, S, Nkv, D,
+                                            (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(),
+                                            cap, e, as));
             ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D, vtb.p, s_ld, vl,
                                 as));
             ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, 1, S, S, Nh, Nkv, D, mask, 0,
                                 0, scale, kPdl, lo, lo, vl, e, as));
         } else {
-            ACB_TRY(dense_forward(L.qkv, false, xp, H, 0, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
-                                  0, sc, s));
+            ACB_TRY(dense_forward(L.qkv, false, hp, H, 0, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
+                                  0, sc, s, &ns_in));
             ACB_TRY(acb_qk_norm_rope(qkv.p, ACB_TYPE_F16, NQKV, q.p, ACB_TYPE_F16, QD, D, 0, S, Nh, D,
                                      (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
                                      as));
@@ -199,10 +198,12 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
         }
         ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
                               0, sc, s));
-        ACB_TRY(acb_rms_norm(hp, ACB_TYPE_F32, H, (const float *) L.post_norm->data, xp, ACB_TYPE_F32, H, S, H, eps,
-                             as));
-        ACB_TRY(dense_forward(L.gu, exact, xp, H, 0, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0,
-                              sc, s));
+        // post_attention_layernorm inside the gate/up projection's producer
+        NormSpec ns_post;
+        ns_post.w   = (const float *) L.post_norm->data;
+        ns_post.eps = eps;
+        ACB_TRY(dense_forward(L.gu, exact, hp, H, 0, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0,
+                              sc, s, &ns_post));
         ACB_TRY(dense_forward(L.down, exact, gu.as<float>(), 2 * F, F, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr,
                               0, 0, sc, s));
     }

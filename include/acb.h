@@ -104,6 +104,16 @@ ACB_API acb_status acb_qk_norm_rope(const void * src, int src_type, int64_t src_
                             int n_heads, int head_dim, const float * norm_w, float eps, const int32_t * pos,
                             const float * rope_table, int max_pos, int * err_flag, acb_stream_t stream);
 
+/* acb_qk_norm_rope into the exact operand planes of the split-precision attention: dst[t][h*128
+ * + d] = f16(v) and dst[lo_offset + same] = f16(v - hi), v the fp32 normalised (and, with a
+ * rope table, rotated) value. head_dim 128; src f32 or f16. One pass instead of an f32 result
+ * followed by acb_act_quant_ex(..., ACB_LAYOUT_PLANES). */
+ACB_API acb_status acb_qk_norm_rope_planes(const void * src, int src_type, int64_t src_tok_stride, uint16_t * dst,
+                                           int64_t dst_tok_stride, int64_t lo_offset, int64_t n_tok, int n_heads,
+                                           int head_dim, const float * norm_w, float eps, const int32_t * pos,
+                                           const float * rope_table, int max_pos, int * err_flag,
+                                           acb_stream_t stream);
+
 /* out[r][i] = silu(g[r][i]) * u[r][i], silu(v) = v / (1 + exp(-v)). g = gu + r*gu_stride,
  * u = g + up_offset (fused [gate(F) | up(F)] rows: up_offset = F, gu_stride = 2F).
  * Replaces ggml_swiglu / ggml_swiglu_split (src/qwen3-enc.h:217,221; src/dit-graph.h:259,264). */
@@ -180,6 +190,19 @@ enum {
 ACB_API acb_status acb_act_quant_ex(const float * x, int64_t x_stride, int64_t up_offset, int64_t rows, int64_t K,
                                     int vec_type, int layout, void * y, int y_type, int64_t y_stride,
                                     int64_t lo_offset, acb_stream_t stream);
+
+/* RMSNorm of each row (times norm_w when given), optionally adaLN-modulated (y = n * (1 + scale)
+ * + shift, scale/shift f32 vectors of one sample every rows_per_sample rows, vec_stride apart),
+ * then quantised exactly as acb_act_quant_ex does (vec_type, layout PLAIN / GEMM_A / PLANES).
+ * Replaces ggml_rms_norm + ggml_mul [+ ggml_mul(1 + scale) + ggml_add(shift)] feeding a
+ * ggml_mul_mat (src/dit-graph.h:150-157, 250-258, src/qwen3-enc.h:80-90) in one pass; results
+ * are bit-identical to acb_rms_norm / acb_adaln_modulate (f32 output) followed by
+ * acb_act_quant_ex. Without norm_w the adaLN form applies no normalisation (as
+ * acb_adaln_modulate). K a multiple of 32 (256 for Q8_K), at most 4096. */
+ACB_API acb_status acb_norm_quant(const float * x, int64_t x_stride, int64_t rows, int64_t K, const float * norm_w,
+                                  float eps, const float * scale, const float * shift, int64_t vec_stride,
+                                  int64_t rows_per_sample, int vec_type, int layout, void * y, int y_type,
+                                  int64_t y_stride, int64_t lo_offset, acb_stream_t stream);
 
 /* Vec-dot type of a weight type (ggml's type_traits_cpu[].vec_dot_type): Q8_0 for Q8_0, Q8_K
  * for Q4_K / Q6_K, the type itself for F16 / BF16 / F32 (F32: the activation stays f32; the

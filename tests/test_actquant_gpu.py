@@ -95,3 +95,46 @@ def test_act_quant_exact_layouts(cuda, layout, vt):
     assert_bitexact(y, want, f"layout {layout}")
     if vt == O.Q8_0:  # f16 scale times a 7-bit integer: the split is exact
         assert np.array_equal(hi.astype(np.float32) + lo.astype(np.float32), v)
+
+
+@pytest.mark.parametrize("vt", [O.Q8_0, O.Q8_K, O.F16, O.BF16])
+@pytest.mark.parametrize("layout", [acb.LAYOUT_PLAIN, acb.LAYOUT_GEMM_A, acb.LAYOUT_PLANES])
+@pytest.mark.parametrize("K", [1024, 2048, 2560])
+def test_norm_quant_matches_unfused(cuda, vt, layout, K):
+    """acb_norm_quant (RMSNorm x w [+ adaLN] fused into the activation quantiser) is bit-identical
+    to acb_rms_norm / acb_adaln_modulate with f32 output followed by acb_act_quant_ex."""
+    import torch
+    if vt == O.BF16 and layout != acb.LAYOUT_PLAIN:
+        pytest.skip("the split layouts are f16")
+    rng = np.random.default_rng(K + vt * 7 + layout)
+    S, T = 3, 37
+    M = S * T
+    x = torch.from_numpy((rng.standard_normal((M, K)) * rng.uniform(0.1, 30, (M, 1))).astype(np.float32)).to(cuda)
+    w = torch.from_numpy((1 + 0.1 * rng.standard_normal(K)).astype(np.float32)).to(cuda)
+    sc = torch.from_numpy((0.2 * rng.standard_normal((S, K))).astype(np.float32)).to(cuda)
+    sh = torch.from_numpy((0.2 * rng.standard_normal((S, K))).astype(np.float32)).to(cuda)
+    # RMSNorm x w
+    got = acb.norm_quant(x, K, w, 1e-6, vt, layout)
+    want = acb.act_quant_ex(acb.rms_norm(x, w, 1e-6), K, vt, layout)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # adaLN: per-sample scale / shift
+    got = acb.norm_quant(x, K, w, 1e-6, vt, layout, scale=sc, shift=sh, rows_per_sample=T, vec_stride=K)
+    xm = acb.adaln_modulate(x.view(S, T, K), w, 1e-6, sc, sh).reshape(M, K)
+    want = acb.act_quant_ex(xm, K, vt, layout)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("rope", [False, True])
+def test_qk_norm_rope_planes_matches_unfused(cuda, rope):
+    """acb_qk_norm_rope_planes == acb_qk_norm_rope (f32) followed by acb_act_quant_ex PLANES, bit for bit."""
+    import torch
+    rng = np.random.default_rng(5 + rope)
+    T, Nh, D = 300, 3, 128
+    src = torch.from_numpy(rng.standard_normal((T, Nh * D + 64)).astype(np.float32) * 3).to(cuda)
+    w = torch.from_numpy((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)).to(cuda)
+    pos = torch.from_numpy(rng.integers(0, 512, T).astype(np.int32)).to(cuda) if rope else None
+    tab = acb.rope_table(512, D, 1e6).to(cuda) if rope else None
+    got = acb.qk_norm_rope_planes(src, Nh, w, 1e-6, pos=pos, rope=tab)
+    ref32 = acb.qk_norm_rope(src, Nh, D, w, 1e-6, pos, tab, out_dtype=torch.float32).reshape(T, Nh * D)
+    want = acb.act_quant_ex(ref32, Nh * D, O.F16, acb.LAYOUT_PLANES)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
