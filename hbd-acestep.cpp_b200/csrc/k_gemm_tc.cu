@@ -33,6 +33,8 @@ namespace acb {
 constexpr int kBN = 256, kBK = 64;
 constexpr int kGemmThreads = 192;
 constexpr int kTmemCols    = 512;
+constexpr int kStgPitch    = 36;                       // floats per staged row (16-byte aligned, conflict-free)
+constexpr int kStgBytes    = 4 * 32 * kStgPitch * 4;   // one 32 x 32 f32 block per epilogue warp
 
 template <bool PAIR> struct GemmCfg {
     static constexpr int      kTileM  = PAIR ? 256 : 128;  // output rows per work tile
@@ -42,7 +44,7 @@ template <bool PAIR> struct GemmCfg {
     static constexpr int      kStage  = kATile + kBTile;
     static constexpr int      kStages = PAIR ? 6 : 4;
     static constexpr uint32_t kTx     = (PAIR ? 2 : 1) * kStage;  // bytes landing per stage
-    static constexpr size_t   kSmem   = (size_t) kStages * kStage + 1024 + 256;
+    static constexpr size_t   kSmem   = (size_t) kStages * kStage + kStgBytes + 1024 + 256;
 };
 
 enum { EPI_PLAIN = 0, EPI_BIAS = 1, EPI_RES = 2, EPI_GATED_RES = 4 };
@@ -65,24 +67,42 @@ struct GemmArgs {
     float *       ws;      // [splits][M][N] f32 partial accumulators
 };
 
-// 32 accumulator columns of one row to a 16-bit C (vector stores when whole and aligned)
-template <int T>
-__device__ __forceinline__ void store_row16(void * C, int64_t off, const float * v, bool full_cols, int left) {
+// up to 4 consecutive columns of one row: one vector access when all 4 are in range and aligned
+template <int T> __device__ __forceinline__ void store_cols(void * C, int64_t off, const float * v, int ncol) {
     using et = typename io<T>::t;
     et * dst = reinterpret_cast<et *>(C) + off;
-    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (ncol == 4 && (reinterpret_cast<uintptr_t>(dst) & (4 * sizeof(et) - 1)) == 0) {
+        if constexpr (T == ACB_TYPE_F32) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+            union {
+                uint2 u;
+                et    e[4];
+            } pk;
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-            vec16<T> pk;
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                pk.v[e] = io<T>::from_f(v[j + e]);
+            for (int j = 0; j < 4; j++) {
+                pk.e[j] = io<T>::from_f(v[j]);
             }
-            *reinterpret_cast<uint4 *>(dst + j) = pk.u;
+            *reinterpret_cast<uint2 *>(dst) = pk.u;
         }
     } else {
-        for (int j = 0; j < 32 && j < left; j++) {
+        for (int j = 0; j < ncol; j++) {
             dst[j] = io<T>::from_f(v[j]);
+        }
+    }
+}
+
+__device__ __forceinline__ void load_cols(const float * src, float * v, int ncol) {
+    if (ncol == 4 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const float4 a = *reinterpret_cast<const float4 *>(src);
+        v[0]           = a.x;
+        v[1]           = a.y;
+        v[2]           = a.z;
+        v[3]           = a.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            v[j] = j < ncol ? src[j] : 0.0f;
         }
     }
 }
@@ -96,7 +116,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * ring = smem;  // kStages * kStage, 1024-aligned tiles (same offsets in both CTAs of a pair)
-    uint64_t * full       = reinterpret_cast<uint64_t *>(smem + Cf::kStages * Cf::kStage);
+    float *    stage_base = reinterpret_cast<float *>(smem + Cf::kStages * Cf::kStage);
+    uint64_t * full       = reinterpret_cast<uint64_t *>(smem + Cf::kStages * Cf::kStage + kStgBytes);
     uint64_t * empty      = full + Cf::kStages;
     uint64_t * tmem_full  = empty + Cf::kStages;
     uint64_t * tmem_empty = tmem_full + 2;
@@ -234,10 +255,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
         }
     } else {
-        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = tile rows
-        const int q    = warp & 3;
-        const int row_in_tile = q * 32 + lane;
-        int       tile = 0;
+        // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 = tile rows. Each 32x32 chunk of raw
+        // accumulators goes through this warp's staging block in shared memory so that global
+        // reads and writes are whole 128-byte row segments (8 lanes x 4 columns per row).
+        const int q     = warp & 3;
+        float *   stg   = stage_base + q * 32 * kStgPitch;
+        const int sub   = lane >> 3;       // row offset within a group of 4 rows
+        const int cc    = (lane & 7) * 4;  // column offset within the chunk
+        int       tile  = 0;
         for (int64_t w = unit; w < n_work; w += n_units, tile++) {
             const int acc = tile & 1;
             if (!ptx::mbar_wait(&tmem_full[acc], (tile >> 1) & 1)) {
@@ -248,76 +273,70 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t t  = w % tiles;
-            const int64_t m  = (t % m_tiles) * Cf::kTileM + (int64_t) rank * 128 + row_in_tile;
-            const int64_t n0 = (t / m_tiles) * kBN;
-            const bool    part = g.splits > 1;  // raw partial of split w / tiles
-            float *       pdst = part ? g.ws + ((w / tiles) * g.M + m) * g.N : nullptr;
-            const float * gate_row = (!part && (g.epi & EPI_GATED_RES))
-                                         ? g.gate + (m < g.M ? (m / g.rows_per_sample) : 0) * g.gate_stride
-                                         : nullptr;
+            const int64_t t      = w % tiles;
+            const int64_t m_base = (t % m_tiles) * Cf::kTileM + (int64_t) rank * 128 + q * 32;
+            const int64_t n0     = (t / m_tiles) * kBN;
+            const bool    part   = g.splits > 1;  // raw partial of split w / tiles
+            float *       pws    = part ? g.ws + (w / tiles) * g.M * g.N : nullptr;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; c++) {
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN + c * 32), r);
                 const int64_t nc = n0 + c * 32;
-                if (m < g.M && nc < g.N) {
-                float v[32];
-#pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    v[j] = __uint_as_float(r[j]);
+                if (nc >= g.N || m_base >= g.M) {
+                    continue;  // warp-uniform: the whole chunk is outside C
                 }
-                const bool full_cols = nc + 32 <= g.N;
-                if (part) {
-                    float * dst = pdst + nc;
-                    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int j = 0; j < 32; j += 4) {
+                    *reinterpret_cast<float4 *>(stg + lane * kStgPitch + j) =
+                        make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                    __uint_as_float(r[j + 3]));
+                }
+                __syncwarp();
+                const int64_t n    = nc + cc;
+                const int     ncol = n < g.N ? (g.N - n < 4 ? (int) (g.N - n) : 4) : 0;
+#pragma unroll 2
+                for (int it = 0; it < 8; it++) {
+                    const int     rr = it * 4 + sub;
+                    const int64_t m  = m_base + rr;
+                    if (m >= g.M || ncol == 0) {
+                        continue;
+                    }
+                    const float4 a    = *reinterpret_cast<const float4 *>(stg + rr * kStgPitch + cc);
+                    float        v[4] = { a.x, a.y, a.z, a.w };
+                    if (part) {
+                        store_cols<ACB_TYPE_F32>(pws, m * g.N + n, v, ncol);
+                        continue;
+                    }
+                    if (g.bias) {
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            if (j < ncol) {
+                                v[j] = __fadd_rn(v[j], g.bias[n + j]);
+                            }
                         }
+                    }
+                    if (g.epi & (EPI_RES | EPI_GATED_RES)) {
+                        float rv[4], gv[4] = { 1.0f, 1.0f, 1.0f, 1.0f };
+                        load_cols(g.res + m * g.ldr + n, rv, ncol);
+                        if (g.epi & EPI_GATED_RES) {
+                            load_cols(g.gate + (m / g.rows_per_sample) * g.gate_stride + n, gv, ncol);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const float o = (g.epi & EPI_GATED_RES) ? __fmul_rn(v[j], gv[j]) : v[j];
+                            v[j]          = __fadd_rn(rv[j], o);
+                        }
+                    }
+                    if (g.c_type == ACB_TYPE_F32) {
+                        store_cols<ACB_TYPE_F32>(g.C, m * g.ldc + n, v, ncol);
+                    } else if (g.c_type == ACB_TYPE_BF16) {
+                        store_cols<ACB_TYPE_BF16>(g.C, m * g.ldc + n, v, ncol);
                     } else {
-                        for (int j = 0; j < 32 && nc + j < g.N; j++) {
-                            dst[j] = v[j];
-                        }
-                    }
-                } else {  // final tile: epilogue and store
-                if (g.bias) {
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        if (full_cols || nc + j < g.N) {
-                            v[j] = __fadd_rn(v[j], g.bias[nc + j]);
-                        }
+                        store_cols<ACB_TYPE_F16>(g.C, m * g.ldc + n, v, ncol);
                     }
                 }
-                if (g.epi & (EPI_RES | EPI_GATED_RES)) {
-                    const float * rr = g.res + m * g.ldr + nc;
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        if (full_cols || nc + j < g.N) {
-                            const float o = (g.epi & EPI_GATED_RES) ? __fmul_rn(v[j], gate_row[nc + j]) : v[j];
-                            v[j]          = __fadd_rn(rr[j], o);
-                        }
-                    }
-                }
-                if (g.c_type == ACB_TYPE_F32) {
-                    float * dst = reinterpret_cast<float *>(g.C) + m * g.ldc + nc;
-                    if (full_cols && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            *reinterpret_cast<float4 *>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                        }
-                    } else {
-                        for (int j = 0; j < 32 && nc + j < g.N; j++) {
-                            dst[j] = v[j];
-                        }
-                    }
-                } else if (g.c_type == ACB_TYPE_BF16) {
-                    store_row16<ACB_TYPE_BF16>(g.C, m * g.ldc + nc, v, full_cols, (int) (g.N - nc));
-                } else {
-                    store_row16<ACB_TYPE_F16>(g.C, m * g.ldc + nc, v, full_cols, (int) (g.N - nc));
-                }
-                }  // final tile
-                }  // valid row and column chunk
+                __syncwarp();
             }
             tc_fence_before();
             __syncwarp();
