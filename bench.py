@@ -564,9 +564,14 @@ def run_gemm_shapes(dev, reps=20, which=None):
             A = torch.randn(M, Kp, device=dev).to(dt)
             B = (torch.randn(N, Kp, device=dev) * 0.02).to(dt)
             C = torch.empty(M, N, device=dev, dtype=torch.float32)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
             for _ in range(3):
                 acb.gemm_bf16(A, B, out=C)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e1.record()
+            torch.cuda.synchronize()
+            # enough launches for ~150 ms of steady-state work (clocks settle under the power cap)
+            reps = max(20, int(150.0 / max(e0.elapsed_time(e1) / 3, 1e-3)))
             e0.record()
             for _ in range(reps):
                 acb.gemm_bf16(A, B, out=C)

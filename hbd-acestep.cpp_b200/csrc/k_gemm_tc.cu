@@ -67,44 +67,45 @@ struct GemmArgs {
     float *       ws;      // [splits][M][N] f32 partial accumulators
 };
 
-// up to 4 consecutive columns of one row: one vector access when all 4 are in range and aligned
-template <int T> __device__ __forceinline__ void store_cols(void * C, int64_t off, const float * v, int ncol) {
+// up to 4 consecutive columns of one row: one vector access when all 4 are in range and aligned.
+// Values travel in a float4 and every index is static, so nothing is placed in local memory.
+__device__ __forceinline__ float f4_get(const float4 & v, int j) {
+    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
+
+template <int T> __device__ __forceinline__ void store_cols(void * C, int64_t off, float4 v, int ncol) {
     using et = typename io<T>::t;
     et * dst = reinterpret_cast<et *>(C) + off;
     if (ncol == 4 && (reinterpret_cast<uintptr_t>(dst) & (4 * sizeof(et) - 1)) == 0) {
         if constexpr (T == ACB_TYPE_F32) {
-            *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4 *>(dst) = v;
         } else {
             union {
                 uint2 u;
                 et    e[4];
             } pk;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                pk.e[j] = io<T>::from_f(v[j]);
-            }
+            pk.e[0]                          = io<T>::from_f(v.x);
+            pk.e[1]                          = io<T>::from_f(v.y);
+            pk.e[2]                          = io<T>::from_f(v.z);
+            pk.e[3]                          = io<T>::from_f(v.w);
             *reinterpret_cast<uint2 *>(dst) = pk.u;
         }
     } else {
-        for (int j = 0; j < ncol; j++) {
-            dst[j] = io<T>::from_f(v[j]);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (j < ncol) {
+                dst[j] = io<T>::from_f(f4_get(v, j));
+            }
         }
     }
 }
 
-__device__ __forceinline__ void load_cols(const float * src, float * v, int ncol) {
+__device__ __forceinline__ float4 load_cols(const float * src, int ncol) {
     if (ncol == 4 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-        const float4 a = *reinterpret_cast<const float4 *>(src);
-        v[0]           = a.x;
-        v[1]           = a.y;
-        v[2]           = a.z;
-        v[3]           = a.w;
-    } else {
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            v[j] = j < ncol ? src[j] : 0.0f;
-        }
+        return *reinterpret_cast<const float4 *>(src);
     }
+    return make_float4(ncol > 0 ? src[0] : 0.0f, ncol > 1 ? src[1] : 0.0f, ncol > 2 ? src[2] : 0.0f,
+                       ncol > 3 ? src[3] : 0.0f);
 }
 
 // ---- the kernel ------------------------------------------------------------------------------------
@@ -302,31 +303,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (m >= g.M || ncol == 0) {
                         continue;
                     }
-                    const float4 a    = *reinterpret_cast<const float4 *>(stg + rr * kStgPitch + cc);
-                    float        v[4] = { a.x, a.y, a.z, a.w };
+                    float4 v = *reinterpret_cast<const float4 *>(stg + rr * kStgPitch + cc);
                     if (part) {
                         store_cols<ACB_TYPE_F32>(pws, m * g.N + n, v, ncol);
                         continue;
                     }
                     if (g.bias) {
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            if (j < ncol) {
-                                v[j] = __fadd_rn(v[j], g.bias[n + j]);
-                            }
-                        }
+                        const float4 bv = load_cols(g.bias + n, ncol);
+                        v.x             = __fadd_rn(v.x, bv.x);
+                        v.y             = __fadd_rn(v.y, bv.y);
+                        v.z             = __fadd_rn(v.z, bv.z);
+                        v.w             = __fadd_rn(v.w, bv.w);
                     }
                     if (g.epi & (EPI_RES | EPI_GATED_RES)) {
-                        float rv[4], gv[4] = { 1.0f, 1.0f, 1.0f, 1.0f };
-                        load_cols(g.res + m * g.ldr + n, rv, ncol);
+                        const float4 rv = load_cols(g.res + m * g.ldr + n, ncol);
                         if (g.epi & EPI_GATED_RES) {
-                            load_cols(g.gate + (m / g.rows_per_sample) * g.gate_stride + n, gv, ncol);
+                            const float4 gv = load_cols(g.gate + (m / g.rows_per_sample) * g.gate_stride + n, ncol);
+                            v.x             = __fmul_rn(v.x, gv.x);
+                            v.y             = __fmul_rn(v.y, gv.y);
+                            v.z             = __fmul_rn(v.z, gv.z);
+                            v.w             = __fmul_rn(v.w, gv.w);
                         }
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const float o = (g.epi & EPI_GATED_RES) ? __fmul_rn(v[j], gv[j]) : v[j];
-                            v[j]          = __fadd_rn(rv[j], o);
-                        }
+                        v.x = __fadd_rn(rv.x, v.x);
+                        v.y = __fadd_rn(rv.y, v.y);
+                        v.z = __fadd_rn(rv.z, v.z);
+                        v.w = __fadd_rn(rv.w, v.w);
                     }
                     if (g.c_type == ACB_TYPE_F32) {
                         store_cols<ACB_TYPE_F32>(g.C, m * g.ldc + n, v, ncol);
