@@ -116,7 +116,7 @@ def lib():
             "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
             "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_norm_quant": (I, [P, I64, I64, I64, P, F, P, P, I64, I64, I, I, P, I, I64, I64, P]),
-            "acb_qk_norm_rope_planes": (I, [P, I, I64, P, I64, I64, I64, I, I, P, F, P, P, I, P, P]),
+            "acb_qk_norm_rope_planes": (I, [P, I, I64, P, I64, I64, I64, I, P, I, P, I, F, P, P, I, P, P]),
             "acb_attn_prefill_split": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I,
                                            I, I, F, I, I64, I64, I64, P]),
             "acb_qwen3_free": (None, [P]),
@@ -569,16 +569,16 @@ def norm_quant(x, K, w, eps, vec_type, layout, scale=None, shift=None, rows_per_
     return out
 
 
-def qk_norm_rope_planes(src, n_heads, w, eps, pos=None, rope=None, err=None, stream=None):
-    """acb_qk_norm_rope_planes: src [T, >= n_heads*128] -> f16 planes [2T, n_heads*128] (hi rows
-    then lo rows)."""
+def qk_norm_rope_planes(src, n_heads, w, eps, pos=None, rope=None, n_k_heads=0, k_w=None, err=None, stream=None):
+    """acb_qk_norm_rope_planes: src [T, >= (n_heads + n_k_heads)*128] -> f16 planes
+    [2T, (n_heads + n_k_heads)*128] (hi rows then lo rows); heads past n_heads use k_w."""
     import torch
-    T, W = src.shape[0], n_heads * 128
+    T, W = src.shape[0], (n_heads + n_k_heads) * 128
     out = torch.empty((2 * T, W), dtype=torch.float16, device=src.device)
     max_pos = rope.shape[0] if rope is not None else 0
     _check("acb_qk_norm_rope_planes", lib().acb_qk_norm_rope_planes(
-        _ptr(src), dtype_id(src), src.stride(0), _ptr(out), W, T * W, T, n_heads, 128, _ptr(w), eps, _ptr(pos),
-        _ptr(rope), max_pos, _ptr(err), _stream(stream)))
+        _ptr(src), dtype_id(src), src.stride(0), _ptr(out), W, T * W, T, n_heads, _ptr(w), n_k_heads, _ptr(k_w), 128,
+        eps, _ptr(pos), _ptr(rope), max_pos, _ptr(err), _stream(stream)))
     return out
 
 

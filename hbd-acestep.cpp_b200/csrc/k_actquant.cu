@@ -195,83 +195,79 @@ __device__ __forceinline__ void split_store(typename io<OT>::t * yr, const float
 // RMSNorm (+ weight) [+ adaLN modulate] of a row followed by the quantisation above, in one pass:
 // ggml_rms_norm -> ggml_mul(w) [-> ggml_mul(1 + scale) -> ggml_add(shift)] and then the
 // from_float of the next ggml_mul_mat (src/dit-graph.h:150-157, 250-258; src/qwen3-enc.h:80-90),
-// with every product and sum rounded as those separate graph nodes round them. One warp per
-// row; lane l holds elements [256c + 8l, 256c + 8l + 8) of chunk c in registers. Without a
-// weight, the adaLN form skips the normalisation (as acb_adaln_modulate does).
-template <int VT, int LAYOUT, int NCH, bool ADALN>
-__global__ void __launch_bounds__(kAqWarps * 32)
-    norm_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t rows, int64_t K, const float * __restrict__ w,
+// with every product and sum rounded as those separate graph nodes round them. One CTA per row,
+// one warp per 256-element chunk (lane l holds elements [256w + 8l, +8) in registers); the
+// row's sum of squares (double) is combined across warps through shared memory in warp order.
+// Without a weight, the adaLN form skips the normalisation (as acb_adaln_modulate does).
+template <int VT, int LAYOUT, bool ADALN>
+__global__ void __launch_bounds__(512)
+    norm_quant_kernel(const float * __restrict__ x, int64_t xs, int64_t K, const float * __restrict__ w,
                       float eps, const float * __restrict__ scale, const float * __restrict__ shift, int64_t vs,
                       int64_t rps, void * __restrict__ y, int64_t ys, int64_t lo_off, bool vec_in, bool vec_out) {
-    const int     lane = threadIdx.x & 31;
-    const int64_t r    = (int64_t) blockIdx.x * kAqWarps + (threadIdx.x >> 5);
-    if (r >= rows) {
-        return;
-    }
-    const float * xr = x + r * xs;
-    float         v[NCH][8];
-    double        ss = 0.0;
-#pragma unroll
-    for (int c = 0; c < NCH; c++) {
-        const int64_t c0 = (int64_t) c * 256 + lane * 8;
-        if (c0 < K) {
-            load8(xr + c0, vec_in, v[c]);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                v[c][e] = 0.0f;
-            }
-        }
+    __shared__ double part[16];
+    const int     lane  = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int64_t r     = blockIdx.x;
+    const int64_t c0    = (int64_t) wid * 256 + lane * 8;
+    const bool    valid = c0 < K;  // K is a multiple of 32: a lane is all in or all out
+    float         v[8];
+    if (valid) {
+        load8(x + r * xs + c0, vec_in, v);
+    } else {
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            ss += (double) __fmul_rn(v[c][e], v[c][e]);
+            v[e] = 0.0f;
         }
     }
     const bool do_norm = !ADALN || w != nullptr;
-    ss                 = warp_sum(ss);
-    const float   sc   = do_norm ? rms_scale(ss, (int) K, eps) : 1.0f;
-    const int64_t smp  = ADALN ? r / rps : 0;
-    constexpr int OT   = VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
-    using et           = typename io<OT>::t;
-#pragma unroll
-    for (int c = 0; c < NCH; c++) {
-        const int64_t c0    = (int64_t) c * 256 + lane * 8;
-        const bool    valid = c0 < K;
-        if (VT != ACB_TYPE_Q8_K && (int64_t) c * 256 >= K) {
-            break;  // warp-uniform: no lane of this chunk is in the row
-        }
-        float f[8];
+    float      sc      = 1.0f;
+    if (do_norm) {
+        double ss = 0.0;
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            f[e] = 0.0f;
+            ss += (double) __fmul_rn(v[e], v[e]);
         }
-        if (valid) {
+        ss = warp_sum(ss);
+        if (lane == 0) {
+            part[wid] = ss;
+        }
+        __syncthreads();
+        double t = 0.0;
+        for (int i = 0; i < nw; i++) {
+            t += part[i];
+        }
+        sc = rms_scale(t, (int) K, eps);
+    }
+    const int64_t smp = ADALN ? r / rps : 0;
+    float         f[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                float t = v[c][e];
-                if (do_norm) {
-                    t = __fmul_rn(t, sc);
-                    if (w) {
-                        t = __fmul_rn(t, __ldg(w + c0 + e));
-                    }
-                }
-                if (ADALN) {
-                    t = __fadd_rn(__fmul_rn(t, __fadd_rn(__ldg(scale + smp * vs + c0 + e), 1.0f)),
-                                  __ldg(shift + smp * vs + c0 + e));
-                }
-                f[e] = t;
-            }
-        }
-        float o[8];
-        quant8<VT>(f, lane, o);
+    for (int e = 0; e < 8; e++) {
+        float t = v[e];
         if (valid) {
-            et * yr = reinterpret_cast<et *>(y) + r * ys + c0;
-            if constexpr (LAYOUT == ACB_LAYOUT_PLAIN) {
-                store8<OT>(yr, o, vec_out);
-            } else {
-                split_store<OT, LAYOUT>(yr, o, K, lo_off, vec_out);
+            if (do_norm) {
+                t = __fmul_rn(t, sc);
+                if (w) {
+                    t = __fmul_rn(t, __ldg(w + c0 + e));
+                }
+            }
+            if (ADALN) {
+                t = __fadd_rn(__fmul_rn(t, __fadd_rn(__ldg(scale + smp * vs + c0 + e), 1.0f)),
+                              __ldg(shift + smp * vs + c0 + e));
             }
         }
+        f[e] = t;
+    }
+    float o[8];
+    quant8<VT>(f, lane, o);
+    if (!valid) {
+        return;
+    }
+    constexpr int OT = VT == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16;
+    using et         = typename io<OT>::t;
+    et * yr          = reinterpret_cast<et *>(y) + r * ys + c0;
+    if constexpr (LAYOUT == ACB_LAYOUT_PLAIN) {
+        store8<OT>(yr, o, vec_out);
+    } else {
+        split_store<OT, LAYOUT>(yr, o, K, lo_off, vec_out);
     }
 }
 
@@ -403,42 +399,24 @@ extern "C" acb_status acb_act_quant_ex(const float * x, int64_t x_stride, int64_
 
 namespace {
 
-template <int VT, int LAYOUT, bool ADALN>
-void launch_nq_nch(int nch, dim3 grid, cudaStream_t st, const float * x, int64_t xs, int64_t rows, int64_t K,
-                   const float * w, float eps, const float * scale, const float * shift, int64_t vs, int64_t rps,
-                   void * y, int64_t ys, int64_t lo_off, bool vin, bool vout) {
-#define ACB_NQ(N)                                                                                                  \
-    norm_quant_kernel<VT, LAYOUT, N, ADALN><<<grid, kAqWarps * 32, 0, st>>>(x, xs, rows, K, w, eps, scale, shift, \
-                                                                             vs, rps, y, ys, lo_off, vin, vout)
-    if (nch <= 4) {
-        ACB_NQ(4);
-    } else if (nch <= 8) {
-        ACB_NQ(8);
-    } else if (nch <= 12) {
-        ACB_NQ(12);
-    } else {
-        ACB_NQ(16);
-    }
-#undef ACB_NQ
-}
-
 template <int VT, bool ADALN>
-void launch_nq_layout(int layout, int nch, dim3 grid, cudaStream_t st, const float * x, int64_t xs, int64_t rows,
-                      int64_t K, const float * w, float eps, const float * scale, const float * shift, int64_t vs,
-                      int64_t rps, void * y, int64_t ys, int64_t lo_off, bool vin, bool vout) {
+void launch_nq_layout(int layout, dim3 grid, dim3 block, cudaStream_t st, const float * x, int64_t xs, int64_t K,
+                      const float * w, float eps, const float * scale, const float * shift, int64_t vs, int64_t rps,
+                      void * y, int64_t ys, int64_t lo_off, bool vin, bool vout) {
+#define ACB_NQL(L)                                                                                                \
+    norm_quant_kernel<VT, L, ADALN><<<grid, block, 0, st>>>(x, xs, K, w, eps, scale, shift, vs, rps, y, ys, lo_off, \
+                                                            vin, vout)
     switch (layout) {
         case ACB_LAYOUT_GEMM_A:
-            launch_nq_nch<VT, ACB_LAYOUT_GEMM_A, ADALN>(nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps,
-                                                        y, ys, lo_off, vin, vout);
+            ACB_NQL(ACB_LAYOUT_GEMM_A);
             break;
         case ACB_LAYOUT_PLANES:
-            launch_nq_nch<VT, ACB_LAYOUT_PLANES, ADALN>(nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps,
-                                                        y, ys, lo_off, vin, vout);
+            ACB_NQL(ACB_LAYOUT_PLANES);
             break;
         default:
-            launch_nq_nch<VT, ACB_LAYOUT_PLAIN, ADALN>(nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps,
-                                                       y, ys, lo_off, vin, vout);
+            ACB_NQL(ACB_LAYOUT_PLAIN);
     }
+#undef ACB_NQL
 }
 
 template <bool ADALN>
@@ -448,10 +426,10 @@ acb_status launch_norm_quant(int vec_type, int layout, const float * x, int64_t 
     const bool vin = (xs % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
     const bool vout =
         (ys % 8 == 0) && (K % 8 == 0) && (lo_off % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
-    const int  nch = (int) ((K + 255) / 256);
-    const dim3 grid((unsigned) ((rows + kAqWarps - 1) / kAqWarps));
+    const dim3 grid((unsigned) rows);
+    const dim3 block((unsigned) (((K + 255) / 256) * 32));
 #define ACB_NQV(V) \
-    launch_nq_layout<V, ADALN>(layout, nch, grid, st, x, xs, rows, K, w, eps, scale, shift, vs, rps, y, ys, lo_off, vin, vout)
+    launch_nq_layout<V, ADALN>(layout, grid, block, st, x, xs, K, w, eps, scale, shift, vs, rps, y, ys, lo_off, vin, vout)
     switch (vec_type) {
         case ACB_TYPE_Q8_0:
             ACB_NQV(ACB_TYPE_Q8_0);

@@ -235,14 +235,12 @@ static acb_status dispatch_row_norm(int ti, int to, const void * x, int64_t xs, 
 // ---- per-head q/k RMSNorm + NeoX RoPE ------------------------------------------------------
 // One warp per (token, head). Lane l owns E = D/64 consecutive elements of the first half
 // starting at l*E and the matching elements of the second half, so each NeoX pair (i, i+D/2)
-// lives in one lane. SPLIT (f16 output): the result is also written as exact hi/lo planes,
-// hi = f16(v) at dst and lo = f16(v - hi) lo_off elements further (the operand planes of the
-// split-precision attention), instead of one rounded copy.
-template <int TI, int TO, int E, bool SPLIT = false>
+// lives in one lane.
+template <int TI, int TO, int E>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const void * __restrict__ src, int64_t sts, void * __restrict__ dst, int64_t dts, int64_t dhs, int64_t dps,
     int64_t n_tok, int n_heads, const float * __restrict__ w, float eps, const int32_t * __restrict__ pos,
-    const float * __restrict__ rope, int max_pos, int * __restrict__ err, int64_t lo_off = 0) {
+    const float * __restrict__ rope, int max_pos, int * __restrict__ err) {
     using ei              = typename io<TI>::t;
     using eo              = typename io<TO>::t;
     constexpr int D       = 64 * E;
@@ -304,11 +302,87 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     for (int e = 0; e < E; e++) {
         d[e]        = io<TO>::from_f(a[e]);
         d[HALF + e] = io<TO>::from_f(b[e]);
-        if constexpr (SPLIT) {
-            d[lo_off + e]        = io<TO>::from_f(__fsub_rn(a[e], io<TO>::to_f(d[e])));
-            d[lo_off + HALF + e] = io<TO>::from_f(__fsub_rn(b[e], io<TO>::to_f(d[HALF + e])));
+    }
+}
+
+// q/k RMSNorm (+ NeoX RoPE) of 128-wide heads into exact hi/lo f16 planes: one warp per
+// (token, head); heads [0, nq) use wq, heads [nq, nq + nk) use wk. Lane l holds elements
+// (2l, 2l+1) of each half (8-byte loads), so each NeoX pair (i, i + 64) is in one lane.
+template <int TI>
+__global__ void __launch_bounds__(256) qk_planes_kernel(const void * __restrict__ src, int64_t sts,
+                                                        uint16_t * __restrict__ dst, int64_t dts, int64_t lo_off,
+                                                        int64_t n_tok, int nq, int nk, const float * __restrict__ wq,
+                                                        const float * __restrict__ wk, float eps,
+                                                        const int32_t * __restrict__ pos,
+                                                        const float * __restrict__ rope, int max_pos,
+                                                        int * __restrict__ err) {
+    using ei           = typename io<TI>::t;
+    const int     lane = threadIdx.x & 31;
+    const int     nh   = nq + nk;
+    const int64_t item = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (item >= n_tok * nh) {
+        return;
+    }
+    const int64_t t = item / nh;
+    const int     h = (int) (item - t * nh);
+    int           p = 0;
+    if (rope) {
+        p = __ldg(pos + t);
+        if (p < 0 || p >= max_pos) {
+            if (lane == 0 && err) {
+                atomicOr(err, ACB_DEVERR_POS_RANGE);
+            }
+            return;
         }
     }
+    const ei * s = reinterpret_cast<const ei *>(src) + t * sts + (int64_t) h * 128 + lane * 2;
+    float      a[2], b[2];
+    if constexpr (TI == ACB_TYPE_F32) {
+        const float2 x = *reinterpret_cast<const float2 *>(s), y = *reinterpret_cast<const float2 *>(s + 64);
+        a[0] = x.x;
+        a[1] = x.y;
+        b[0] = y.x;
+        b[1] = y.y;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            a[e] = io<TI>::to_f(s[e]);
+            b[e] = io<TI>::to_f(s[64 + e]);
+        }
+    }
+    const float * w = h < nq ? wq : wk;
+    if (w) {
+        double ss = (double) __fmul_rn(a[0], a[0]);
+        ss += (double) __fmul_rn(a[1], a[1]);
+        ss += (double) __fmul_rn(b[0], b[0]);
+        ss += (double) __fmul_rn(b[1], b[1]);
+        ss             = warp_sum(ss);
+        const float sc = rms_scale(ss, 128, eps);
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * 2 + e));
+            b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(w + 64 + lane * 2 + e));
+        }
+    }
+    if (rope) {
+        const float4 c  = __ldg(reinterpret_cast<const float4 *>(rope + (int64_t) p * 128 + 4 * lane));
+        const float  cs[2] = { c.x, c.z }, sn[2] = { c.y, c.w };
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const float x0 = a[e], x1 = b[e];
+            a[e]           = __fsub_rn(__fmul_rn(x0, cs[e]), __fmul_rn(x1, sn[e]));
+            b[e]           = __fadd_rn(__fmul_rn(x0, sn[e]), __fmul_rn(x1, cs[e]));
+        }
+    }
+    uint16_t *    d  = dst + t * dts + (int64_t) h * 128 + lane * 2;
+    const __half2 ah = __floats2half2_rn(a[0], a[1]), bh = __floats2half2_rn(b[0], b[1]);
+    const float2  af = __half22float2(ah), bf = __half22float2(bh);
+    const __half2 al = __floats2half2_rn(__fsub_rn(a[0], af.x), __fsub_rn(a[1], af.y));
+    const __half2 bl = __floats2half2_rn(__fsub_rn(b[0], bf.x), __fsub_rn(b[1], bf.y));
+    *reinterpret_cast<__half2 *>(d)               = ah;
+    *reinterpret_cast<__half2 *>(d + 64)          = bh;
+    *reinterpret_cast<__half2 *>(d + lo_off)      = al;
+    *reinterpret_cast<__half2 *>(d + lo_off + 64) = bl;
 }
 
 template <int TI, int TO>
@@ -404,11 +478,13 @@ extern "C" acb_status acb_qk_norm_rope(const void * src, int src_type, int64_t s
 }
 
 extern "C" acb_status acb_qk_norm_rope_planes(const void * src, int src_type, int64_t src_tok_stride, uint16_t * dst,
-                                              int64_t dst_tok_stride, int64_t lo_offset, int64_t n_tok, int n_heads,
-                                              int head_dim, const float * norm_w, float eps, const int32_t * pos,
-                                              const float * rope_table, int max_pos, int * err_flag,
-                                              acb_stream_t stream) {
-    if (!src || !dst || n_tok < 0 || n_heads <= 0 || lo_offset <= 0 || dst_tok_stride < (int64_t) n_heads * head_dim) {
+                                              int64_t dst_tok_stride, int64_t lo_offset, int64_t n_tok, int n_q_heads,
+                                              const float * q_norm_w, int n_k_heads, const float * k_norm_w,
+                                              int head_dim, float eps, const int32_t * pos, const float * rope_table,
+                                              int max_pos, int * err_flag, acb_stream_t stream) {
+    const int nh = n_q_heads + n_k_heads;
+    if (!src || !dst || n_tok < 0 || n_q_heads < 0 || n_k_heads < 0 || nh <= 0 || lo_offset <= 0 ||
+        src_tok_stride < (int64_t) nh * head_dim || dst_tok_stride < (int64_t) nh * head_dim) {
         return ACB_ERR_INVALID_ARG;
     }
     if (rope_table && (!pos || max_pos <= 0)) {
@@ -417,20 +493,26 @@ extern "C" acb_status acb_qk_norm_rope_planes(const void * src, int src_type, in
     if (head_dim != 128 || (src_type != ACB_TYPE_F32 && src_type != ACB_TYPE_F16)) {
         return ACB_ERR_UNSUPPORTED;
     }
+    // 8-byte source loads and 4-byte plane stores
+    const int es = src_type == ACB_TYPE_F32 ? 4 : 2;
+    if (reinterpret_cast<uintptr_t>(src) % (2 * es) || (src_tok_stride * es) % (2 * es) ||
+        reinterpret_cast<uintptr_t>(dst) % 4 || dst_tok_stride % 2 || lo_offset % 2) {
+        return ACB_ERR_UNSUPPORTED;
+    }
     if (n_tok == 0) {
         return ACB_OK;
     }
-    const int64_t items = n_tok * n_heads;
+    const int64_t items = n_tok * nh;
     const dim3    grid((unsigned) ((items + 7) / 8));
     cudaStream_t  st = (cudaStream_t) stream;
     if (src_type == ACB_TYPE_F32) {
-        qk_norm_rope_kernel<ACB_TYPE_F32, ACB_TYPE_F16, 2, true><<<grid, 256, 0, st>>>(
-            src, src_tok_stride, dst, dst_tok_stride, head_dim, 0, n_tok, n_heads, norm_w, eps, pos, rope_table,
-            max_pos, err_flag, lo_offset);
+        qk_planes_kernel<ACB_TYPE_F32><<<grid, 256, 0, st>>>(src, src_tok_stride, dst, dst_tok_stride, lo_offset, n_tok,
+                                                             n_q_heads, n_k_heads, q_norm_w, k_norm_w, eps, pos,
+                                                             rope_table, max_pos, err_flag);
     } else {
-        qk_norm_rope_kernel<ACB_TYPE_F16, ACB_TYPE_F16, 2, true><<<grid, 256, 0, st>>>(
-            src, src_tok_stride, dst, dst_tok_stride, head_dim, 0, n_tok, n_heads, norm_w, eps, pos, rope_table,
-            max_pos, err_flag, lo_offset);
+        qk_planes_kernel<ACB_TYPE_F16><<<grid, 256, 0, st>>>(src, src_tok_stride, dst, dst_tok_stride, lo_offset, n_tok,
+                                                             n_q_heads, n_k_heads, q_norm_w, k_norm_w, eps, pos,
+                                                             rope_table, max_pos, err_flag);
     }
     return launch_status();
 }

@@ -285,11 +285,9 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
         const int64_t lo = (int64_t) R * W;
         uint16_t *    hi = planes.as<uint16_t>();
         const int64_t vl = (int64_t) Ng * KD * s_ld;
-        ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, R, Nh, D, (const float *) L.sa_q_norm->data,
-                                        eps, pos.as<int32_t>(), rope.as<float>(), S, e, as));
-        ACB_TRY(acb_qk_norm_rope_planes(q32 + QD, ACB_TYPE_F32, NQKV, hi + QD, W, lo, R, Nkv, D,
-                                        (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S,
-                                        e, as));
+        ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, R, Nh, (const float *) L.sa_q_norm->data,
+                                        Nkv, (const float *) L.sa_k_norm->data, D, eps, pos.as<int32_t>(),
+                                        rope.as<float>(), S, e, as));
         ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, vl, as));
         ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, Ng, S, S, Nh, Nkv, D, mask,
                             c.sliding_window, 0, scale, kPdl, lo, lo, vl, e, as));
@@ -322,8 +320,8 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     if (exact) {
         const int64_t lo = (int64_t) R * QD;
         uint16_t *    qh = planes.as<uint16_t>();
-        ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, D, (const float *) L.ca_q_norm->data,
-                                        eps, nullptr, nullptr, 0, e, as));
+        ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, (const float *) L.ca_q_norm->data, 0,
+                                        nullptr, D, eps, nullptr, nullptr, 0, e, as));
         ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
                             0, scale, kPdl, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
     } else {

@@ -173,11 +173,9 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
             const int64_t lo = (int64_t) cap * W;
             const int64_t vl = (int64_t) KD * s_ld;
             uint16_t *    hi = planes.as<uint16_t>();
-            ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, S, Nh, D, (const float *) L.q_norm->data,
-                                            eps, pos.as<int32_t>(), rope.as<float>(), cap, e, as));
-            ACB_TRY(acb_qk_norm_rope_planes(q32 + QD, ACB_TYPE_F32, NQKV, hi + QD, W, lo, S, Nkv, D,
-                                            (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(),
-                                            cap, e, as));
+            ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, S, Nh, (const float *) L.q_norm->data,
+                                            Nkv, (const float *) L.k_norm->data, D, eps, pos.as<int32_t>(),
+                                            rope.as<float>(), cap, e, as));
             ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D, vtb.p, s_ld, vl,
                                 as));
             ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, 1, S, S, Nh, Nkv, D, mask, 0,

@@ -104,15 +104,17 @@ ACB_API acb_status acb_qk_norm_rope(const void * src, int src_type, int64_t src_
                             int n_heads, int head_dim, const float * norm_w, float eps, const int32_t * pos,
                             const float * rope_table, int max_pos, int * err_flag, acb_stream_t stream);
 
-/* acb_qk_norm_rope into the exact operand planes of the split-precision attention: dst[t][h*128
- * + d] = f16(v) and dst[lo_offset + same] = f16(v - hi), v the fp32 normalised (and, with a
- * rope table, rotated) value. head_dim 128; src f32 or f16. One pass instead of an f32 result
- * followed by acb_act_quant_ex(..., ACB_LAYOUT_PLANES). */
+/* acb_qk_norm_rope into the exact operand planes of the split-precision attention, for the q
+ * heads and the k heads of a fused qkv row in one launch: heads [0, n_q_heads) are normalised
+ * with q_norm_w, heads [n_q_heads, n_q_heads + n_k_heads) with k_norm_w (src head h at column
+ * h*128), then rotated when a rope table is given; dst[t][h*128 + d] = f16(v) and
+ * dst[lo_offset + same] = f16(v - hi), v the fp32 result. head_dim 128; src f32 or f16. One
+ * pass instead of f32 results followed by acb_act_quant_ex(..., ACB_LAYOUT_PLANES). */
 ACB_API acb_status acb_qk_norm_rope_planes(const void * src, int src_type, int64_t src_tok_stride, uint16_t * dst,
-                                           int64_t dst_tok_stride, int64_t lo_offset, int64_t n_tok, int n_heads,
-                                           int head_dim, const float * norm_w, float eps, const int32_t * pos,
-                                           const float * rope_table, int max_pos, int * err_flag,
-                                           acb_stream_t stream);
+                                           int64_t dst_tok_stride, int64_t lo_offset, int64_t n_tok, int n_q_heads,
+                                           const float * q_norm_w, int n_k_heads, const float * k_norm_w,
+                                           int head_dim, float eps, const int32_t * pos, const float * rope_table,
+                                           int max_pos, int * err_flag, acb_stream_t stream);
 
 /* out[r][i] = silu(g[r][i]) * u[r][i], silu(v) = v / (1 + exp(-v)). g = gu + r*gu_stride,
  * u = g + up_offset (fused [gate(F) | up(F)] rows: up_offset = F, gu_stride = 2F).

@@ -126,15 +126,24 @@ def test_norm_quant_matches_unfused(cuda, vt, layout, K):
 
 @pytest.mark.parametrize("rope", [False, True])
 def test_qk_norm_rope_planes_matches_unfused(cuda, rope):
-    """acb_qk_norm_rope_planes == acb_qk_norm_rope (f32) followed by acb_act_quant_ex PLANES, bit for bit."""
+    """acb_qk_norm_rope_planes (q heads and k heads with their own weights, one launch) ==
+    acb_qk_norm_rope (f32) per head group followed by acb_act_quant_ex PLANES, bit for bit."""
     import torch
     rng = np.random.default_rng(5 + rope)
-    T, Nh, D = 300, 3, 128
-    src = torch.from_numpy(rng.standard_normal((T, Nh * D + 64)).astype(np.float32) * 3).to(cuda)
-    w = torch.from_numpy((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)).to(cuda)
+    T, Nq, Nk, D = 300, 3, 2, 128
+    src = torch.from_numpy(rng.standard_normal((T, (Nq + Nk) * D + 64)).astype(np.float32) * 3).to(cuda)
+    wq = torch.from_numpy((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)).to(cuda)
+    wk = torch.from_numpy((1 + 0.1 * rng.standard_normal(D)).astype(np.float32)).to(cuda)
     pos = torch.from_numpy(rng.integers(0, 512, T).astype(np.int32)).to(cuda) if rope else None
     tab = acb.rope_table(512, D, 1e6).to(cuda) if rope else None
-    got = acb.qk_norm_rope_planes(src, Nh, w, 1e-6, pos=pos, rope=tab)
-    ref32 = acb.qk_norm_rope(src, Nh, D, w, 1e-6, pos, tab, out_dtype=torch.float32).reshape(T, Nh * D)
-    want = acb.act_quant_ex(ref32, Nh * D, O.F16, acb.LAYOUT_PLANES)
+    got = acb.qk_norm_rope_planes(src, Nq, wq, 1e-6, pos=pos, rope=tab, n_k_heads=Nk, k_w=wk)
+    rq = acb.qk_norm_rope(src, Nq, D, wq, 1e-6, pos, tab, out_dtype=torch.float32).reshape(T, Nq * D)
+    rk = acb.qk_norm_rope(src[:, Nq * D:], Nk, D, wk, 1e-6, pos, tab, out_dtype=torch.float32).reshape(T, Nk * D)
+    ref32 = torch.cat([rq, rk], dim=1).contiguous()
+    want = acb.act_quant_ex(ref32, (Nq + Nk) * D, O.F16, acb.LAYOUT_PLANES)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # q heads only (the cross-attention form)
+    got = acb.qk_norm_rope_planes(src, Nq, wq, 1e-6)
+    want = acb.act_quant_ex(acb.qk_norm_rope(src, Nq, D, wq, 1e-6, None, None, out_dtype=torch.float32)
+                            .reshape(T, Nq * D).contiguous(), Nq * D, O.F16, acb.LAYOUT_PLANES)
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
