@@ -238,7 +238,17 @@ __global__ void __launch_bounds__(512)
         sc = rms_scale(t, (int) K, eps);
     }
     const int64_t smp = ADALN ? r / rps : 0;
-    float         f[8];
+    float         f[8], wv[8], a[8], b[8];
+    if (valid) {
+        // the weight and modulation vectors: 16-byte loads when aligned (vec_in covers them)
+        if (w) {
+            load8(w + c0, vec_in, wv);
+        }
+        if (ADALN) {
+            load8(scale + smp * vs + c0, vec_in, a);
+            load8(shift + smp * vs + c0, vec_in, b);
+        }
+    }
 #pragma unroll
     for (int e = 0; e < 8; e++) {
         float t = v[e];
@@ -246,12 +256,11 @@ __global__ void __launch_bounds__(512)
             if (do_norm) {
                 t = __fmul_rn(t, sc);
                 if (w) {
-                    t = __fmul_rn(t, __ldg(w + c0 + e));
+                    t = __fmul_rn(t, wv[e]);
                 }
             }
             if (ADALN) {
-                t = __fadd_rn(__fmul_rn(t, __fadd_rn(__ldg(scale + smp * vs + c0 + e), 1.0f)),
-                              __ldg(shift + smp * vs + c0 + e));
+                t = __fadd_rn(__fmul_rn(t, __fadd_rn(a[e], 1.0f)), b[e]);
             }
         }
         f[e] = t;
@@ -423,7 +432,9 @@ template <bool ADALN>
 acb_status launch_norm_quant(int vec_type, int layout, const float * x, int64_t xs, int64_t rows, int64_t K,
                              const float * w, float eps, const float * scale, const float * shift, int64_t vs,
                              int64_t rps, void * y, int64_t ys, int64_t lo_off, cudaStream_t st) {
-    const bool vin = (xs % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+    const bool vin = (xs % 4 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(w) % 16 == 0) && (reinterpret_cast<uintptr_t>(scale) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(shift) % 16 == 0) && vs % 4 == 0;
     const bool vout =
         (ys % 8 == 0) && (K % 8 == 0) && (lo_off % 8 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0);
     const dim3 grid((unsigned) rows);

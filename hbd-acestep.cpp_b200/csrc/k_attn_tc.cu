@@ -4,16 +4,19 @@
 //     O[b,i,h,:] = softmax_j( Q[b,i,h,:] . K[b,j,h/G,:] * scale + mask(i,j) ) V[b,j,h/G,:]
 //
 // One CTA per (128 queries, head, batch), 6 warps:
-//   warp 0      TMA: the Q tile once, then key blocks of 64 (K [64][128] and V^T [128][64]) into a
-//               2-3 stage ring, all 128-byte swizzled K-major tiles;
+//   warp 0      TMA: the Q tile once, then key blocks of 64: K [64][128] and V^T [128][64] into two
+//               separate 2-3 stage rings (a K stage is released as soon as its scores are
+//               computed, a V stage after P.V), all 128-byte swizzled K-major tiles;
 //   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma: S = Q.K^T (M=128 queries,
 //               N=64 keys) into one of two S buffers, and O += P.V (M=128, N=128 head dims) into
 //               the O accumulator; S for block i+2 is issued right after P.V of block i, so the
 //               tensor cores compute the next scores while the softmax of block i+1 runs;
-//   warps 2..5  softmax, one thread per query row (its TMEM lane): scores from TMEM, mask, online
-//               max / sum in fp32 with exp2 (scale folded into log2 e), rescale of the O row in
-//               TMEM when the max grows, P written as a swizzled f16 operand tile; at the end O
-//               divided by the row sum and stored.
+//   warps 2..5  softmax, one thread per query row (its TMEM lane): scores from TMEM, the mask only
+//               on blocks that cross a boundary, online max / sum in fp32 with one FFMA and one
+//               ex2 per score (scale folded into log2 e); the reference max moves (and the O row
+//               in TMEM is rescaled) only when the block max exceeds it by more than 2^8, so P <=
+//               256; P written as a swizzled f16 operand tile; at the end O divided by the row
+//               sum and stored.
 // SPLIT: every operand comes as f16 hi and lo planes (hi + lo = the f32 value) and each product is
 // lo.hi + hi.lo + hi.hi, P split the same way -- f32-accurate attention (the reference CPU build's
 // qwen3_attn_f32 / dit_attn_f32). Every wait is bounded; on a timeout the kernel records
@@ -44,15 +47,26 @@ struct AttnTcArgs {
 };
 
 template <bool SPLIT> struct TcLayout {
-    static constexpr int NP    = SPLIT ? 2 : 1;         // operand planes
-    static constexpr int QB    = NP * 2 * 16384;        // Q: plane x d-chunk x [128][64]
-    static constexpr int KB    = NP * 2 * 8192;         // K block: plane x d-chunk x [64][64]
-    static constexpr int VB    = NP * 16384;            // V^T block: plane x [128][64]
-    static constexpr int SB    = KB + VB;               // one ring stage
-    static constexpr int NS    = SPLIT ? 2 : 3;         // ring stages
-    static constexpr int PB    = NP * 16384;            // P: plane x [128][64]
-    static constexpr int TOTAL = QB + NS * SB + PB;     // 224 KB split, 144 KB otherwise
+    static constexpr int NP    = SPLIT ? 2 : 1;               // operand planes
+    static constexpr int QB    = NP * 2 * 16384;              // Q: plane x d-chunk x [128][64]
+    static constexpr int KB    = NP * 2 * 8192;               // K block: plane x d-chunk x [64][64]
+    static constexpr int VB    = NP * 16384;                  // V^T block: plane x [128][64]
+    static constexpr int NK    = SPLIT ? 2 : 3;               // K ring stages
+    static constexpr int NV    = SPLIT ? 2 : 3;               // V ring stages
+    static constexpr int PB    = NP * 16384;                  // P: plane x [128][64]
+    static constexpr int TOTAL = QB + NK * KB + NV * VB + PB;  // 224 KB split, 144 KB otherwise
 };
+
+// 2^x on the special-function unit (relative error ~2^-22; -inf -> +0, denormal results flush to 0)
+__device__ __forceinline__ float ex2_fast(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// lazy rescaling: the reference max of a row moves only when a block max exceeds it by more than
+// this many powers of two
+constexpr float kRescaleLog2 = 8.0f;
 
 __device__ __forceinline__ bool tc_wait(uint64_t * bar, uint32_t parity, volatile int * abort_flag, int * err) {
     if (*abort_flag) {
@@ -78,12 +92,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t * smem   = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t * sQ     = smem;
-    uint8_t * sStage = smem + Lay::QB;
-    uint8_t * sP     = sStage + Lay::NS * Lay::SB;
+    uint8_t * sK     = smem + Lay::QB;
+    uint8_t * sV     = sK + Lay::NK * Lay::KB;
+    uint8_t * sP     = sV + Lay::NV * Lay::VB;
     uint64_t * q_full   = reinterpret_cast<uint64_t *>(sP + Lay::PB);
-    uint64_t * kv_full  = q_full + 1;
-    uint64_t * kv_empty = kv_full + Lay::NS;
-    uint64_t * s_full   = kv_empty + Lay::NS;
+    uint64_t * k_full   = q_full + 1;
+    uint64_t * k_empty  = k_full + Lay::NK;
+    uint64_t * v_full   = k_empty + Lay::NK;
+    uint64_t * v_empty  = v_full + Lay::NV;
+    uint64_t * s_full   = v_empty + Lay::NV;
     uint64_t * p_full   = s_full + 2;
     uint64_t * pv_done  = p_full + 1;
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(pv_done + 1);
@@ -108,9 +125,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         abort_flag = 0;
         ptx::mbar_init(q_full, 1);
-        for (int s = 0; s < Lay::NS; s++) {
-            ptx::mbar_init(&kv_full[s], 1);
-            ptx::mbar_init(&kv_empty[s], 1);
+        for (int s = 0; s < Lay::NK; s++) {
+            ptx::mbar_init(&k_full[s], 1);
+            ptx::mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < Lay::NV; s++) {
+            ptx::mbar_init(&v_full[s], 1);
+            ptx::mbar_init(&v_empty[s], 1);
         }
         ptx::mbar_init(&s_full[0], 1);
         ptx::mbar_init(&s_full[1], 1);
@@ -142,21 +163,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             for (int i = 0; i < nblk; i++) {
-                const int s = i % Lay::NS;
-                if (i >= Lay::NS && !tc_wait(&kv_empty[s], ((i / Lay::NS) - 1) & 1, &abort_flag, a.err)) {
+                const int key0 = (kb_lo + i) * kTcBK;
+                const int sk = i % Lay::NK, sv = i % Lay::NV;
+                if (i >= Lay::NK && !tc_wait(&k_empty[sk], ((i / Lay::NK) - 1) & 1, &abort_flag, a.err)) {
                     break;
                 }
-                const int key0 = (kb_lo + i) * kTcBK;
-                uint8_t * st   = sStage + s * Lay::SB;
-                ptx::mbar_arrive_expect_tx(&kv_full[s], Lay::SB);
+                uint8_t * kst = sK + sk * Lay::KB;
+                ptx::mbar_arrive_expect_tx(&k_full[sk], Lay::KB);
                 for (int p = 0; p < Lay::NP; p++) {
                     for (int c = 0; c < 2; c++) {
-                        tma_load_2d(st + (p * 2 + c) * 8192, p ? &mkl : &mk, hk * kTcD + c * 64, b * a.Skv + key0,
-                                    &kv_full[s]);
+                        tma_load_2d(kst + (p * 2 + c) * 8192, p ? &mkl : &mk, hk * kTcD + c * 64, b * a.Skv + key0,
+                                    &k_full[sk]);
                     }
                 }
+                if (i >= Lay::NV && !tc_wait(&v_empty[sv], ((i / Lay::NV) - 1) & 1, &abort_flag, a.err)) {
+                    break;
+                }
+                uint8_t * vst = sV + sv * Lay::VB;
+                ptx::mbar_arrive_expect_tx(&v_full[sv], Lay::VB);
                 for (int p = 0; p < Lay::NP; p++) {
-                    tma_load_2d(st + Lay::KB + p * 16384, p ? &mvl : &mv, key0, (b * a.Nkv + hk) * kTcD, &kv_full[s]);
+                    tma_load_2d(vst + p * 16384, p ? &mvl : &mv, key0, (b * a.Nkv + hk) * kTcD, &v_full[sv]);
                 }
             }
         }
@@ -171,12 +197,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int          pa[3]  = { SPLIT ? 1 : 0, 0, 0 };
             const int          pb[3]  = { 0, SPLIT ? 1 : 0, 0 };
             auto issue_s = [&](int i) -> bool {
-                const int s = i % Lay::NS;
-                if (!tc_wait(&kv_full[s], (i / Lay::NS) & 1, &abort_flag, a.err)) {
+                const int sk = i % Lay::NK;
+                if (!tc_wait(&k_full[sk], (i / Lay::NK) & 1, &abort_flag, a.err)) {
                     return false;
                 }
                 tc_fence_after();
-                const uint32_t st  = ptx::smem_u32(sStage + s * Lay::SB);
+                const uint32_t st  = ptx::smem_u32(sK + sk * Lay::KB);
                 const uint32_t tS  = tmem + (uint32_t) ((i & 1) * kTcBK);
                 uint32_t       acc = 0;
                 for (int pr = 0; pr < n_prod; pr++) {
@@ -190,6 +216,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
                 umma_commit(&s_full[i & 1]);
+                umma_commit(&k_empty[sk]);  // this K block is consumed
                 return true;
             };
             bool ok = issue_s(0) && (nblk < 2 || issue_s(1));
@@ -197,9 +224,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (!tc_wait(p_full, i & 1, &abort_flag, a.err)) {
                     break;
                 }
+                const int sv = i % Lay::NV;
+                if (!tc_wait(&v_full[sv], (i / Lay::NV) & 1, &abort_flag, a.err)) {
+                    break;
+                }
                 tc_fence_after();
-                const int      s   = i % Lay::NS;
-                const uint32_t vt  = ptx::smem_u32(sStage + s * Lay::SB + Lay::KB);
+                const uint32_t vt  = ptx::smem_u32(sV + sv * Lay::VB);
                 uint32_t       acc = i > 0 ? 1u : 0u;
                 for (int pr = 0; pr < n_prod; pr++) {
 #pragma unroll
@@ -211,7 +241,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
                 umma_commit(pv_done);
-                umma_commit(&kv_empty[s]);  // K and V of this block are consumed
+                umma_commit(&v_empty[sv]);  // this V block is consumed
                 if (i + 2 < nblk) {
                     ok = issue_s(i + 2);
                 }
@@ -236,26 +266,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK), r);
             tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK + 32), r + 32);
             const int key0 = (kb_lo + i) * kTcBK;
-            float     mx   = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < kTcBK; c++) {
-                const int j  = key0 + c;
-                bool      in = j < a.Skv;
-                if (MASK == TC_MASK_CAUSAL) {
-                    in = in && j <= iq + a.causal_off;
-                } else if (MASK == TC_MASK_WINDOW) {
-                    in = in && (iq > j ? iq - j : j - iq) <= a.window;
-                }
-                const float v = in ? __uint_as_float(r[c]) * a.scale_log2 : -INFINITY;
-                r[c]          = __float_as_uint(v);
-                mx            = fmaxf(mx, v);
+            // the mask, only on a block that crosses a boundary for this row
+            bool need = key0 + kTcBK > a.Skv;
+            if (MASK == TC_MASK_CAUSAL) {
+                need = need || key0 + kTcBK - 1 > iq + a.causal_off;
+            } else if (MASK == TC_MASK_WINDOW) {
+                need = need || key0 < iq - a.window || key0 + kTcBK - 1 > iq + a.window;
             }
-            const float m_new = fmaxf(m, mx);
-            const float alpha = (m == -INFINITY || m_new == -INFINITY) ? 1.0f : exp2f(m - m_new);
-            float       ls    = 0.0f;
+            if (need) {
+#pragma unroll
+                for (int c = 0; c < kTcBK; c++) {
+                    const int j  = key0 + c;
+                    bool      in = j < a.Skv;
+                    if (MASK == TC_MASK_CAUSAL) {
+                        in = in && j <= iq + a.causal_off;
+                    } else if (MASK == TC_MASK_WINDOW) {
+                        in = in && (iq > j ? iq - j : j - iq) <= a.window;
+                    }
+                    if (!in) {
+                        r[c] = __float_as_uint(-INFINITY);
+                    }
+                }
+            }
+            float mx = -INFINITY;
 #pragma unroll
             for (int c = 0; c < kTcBK; c++) {
-                const float p = m_new == -INFINITY ? 0.0f : exp2f(__uint_as_float(r[c]) - m_new);
+                mx = fmaxf(mx, __uint_as_float(r[c]));
+            }
+            // running reference max (log2 domain); moves only when exceeded by > 2^kRescaleLog2
+            const float mb    = mx * a.scale_log2;
+            float       alpha = 1.0f;
+            bool        resc  = false;
+            if (m == -INFINITY) {
+                m = mb;  // no mass accumulated yet: O is still zero
+            } else if (mb > m + kRescaleLog2) {
+                alpha = ex2_fast(m - mb);
+                m     = mb;
+                resc  = true;
+            }
+            const float nm = -m;
+            float       ls = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kTcBK; c++) {
+                const float p = m == -INFINITY ? 0.0f : ex2_fast(fmaf(__uint_as_float(r[c]), a.scale_log2, nm));
                 r[c]          = __float_as_uint(p);
                 ls += p;
             }
@@ -266,7 +319,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+                if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
                     for (int c = 0; c < kTcD / 32; c++) {
                         uint32_t o[32];
@@ -280,7 +333,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             l = l * alpha + ls;
-            m = m_new;
             // P row into the swizzled [128][64] operand tile(s): 16-byte unit u of row `row` goes to
             // unit u ^ (row % 8) (128-byte swizzle, rows 128 bytes apart)
 #pragma unroll
