@@ -11,12 +11,14 @@
 //               N=64 keys) into one of two S buffers, and O += P.V (M=128, N=128 head dims) into
 //               the O accumulator; S for block i+2 is issued right after P.V of block i, so the
 //               tensor cores compute the next scores while the softmax of block i+1 runs;
-//   warps 2..5  softmax, one thread per query row (its TMEM lane): scores from TMEM, the mask only
-//               on blocks that cross a boundary, online max / sum in fp32 with one FFMA and one
-//               ex2 per score (scale folded into log2 e); the reference max moves (and the O row
-//               in TMEM is rescaled) only when the block max exceeds it by more than 2^8, so P <=
-//               256; P written as a swizzled f16 operand tile; at the end O divided by the row
-//               sum and stored.
+//   warps 2..9  softmax, two threads per query row (its TMEM lane; warps w and w+4 share a lane
+//               quarter and take 32 of the 64 key columns each): scores from TMEM, the mask only
+//               on blocks that cross a boundary, the block max combined by the pair through
+//               shared memory, one FFMA and one ex2 per score (scale folded into log2 e); the
+//               reference max moves (and the O row in TMEM is rescaled, each thread its 64
+//               columns) only when the block max exceeds it by more than 2^8, so P <= 256; P
+//               written as a swizzled f16 operand tile; at the end O divided by the row sum and
+//               stored.
 // SPLIT: every operand comes as f16 hi and lo planes (hi + lo = the f32 value) and each product is
 // lo.hi + hi.lo + hi.hi, P split the same way -- f32-accurate attention (the reference CPU build's
 // qwen3_attn_f32 / dit_attn_f32). Every wait is bounded; on a timeout the kernel records
@@ -32,7 +34,7 @@ namespace acb {
 constexpr int kTcBQ      = 128;  // queries per CTA = TMEM lanes
 constexpr int kTcBK      = 64;   // keys per block
 constexpr int kTcD       = 128;  // head dim
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
 
 enum { TC_MASK_NONE = 0, TC_MASK_CAUSAL = 1, TC_MASK_WINDOW = 2 };
 
@@ -103,8 +105,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t * s_full   = v_empty + Lay::NV;
     uint64_t * p_full   = s_full + 2;
     uint64_t * pv_done  = p_full + 1;
-    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(pv_done + 1);
+    uint64_t * xbar     = pv_done + 1;  // [4]: softmax pair exchange, one per TMEM lane quarter
+    uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
     __shared__ volatile int abort_flag;
+    __shared__ float        xchg[2 * 2 * kTcBQ];  // softmax pair exchange: [parity][half][row]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -135,8 +139,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         ptx::mbar_init(&s_full[0], 1);
         ptx::mbar_init(&s_full[1], 1);
-        ptx::mbar_init(p_full, 4);  // one arrival per softmax warp
+        ptx::mbar_init(p_full, 8);  // one arrival per softmax warp
         ptx::mbar_init(pv_done, 1);
+        for (int x = 0; x < 4; x++) {
+            ptx::mbar_init(&xbar[x], 2);  // the two warps of a pair
+        }
         ptx::fence_mbar_init();
         tma_prefetch_desc(&mq);
         tma_prefetch_desc(&mk);
@@ -248,34 +255,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
     } else {
-        // softmax: thread = query row (its TMEM lane)
+        // softmax: two threads per query row. Warp w (2..9) reads TMEM lane quarter w % 4; half
+        // hf = (w - 2) / 4 owns key columns [32 hf, 32 hf + 32) of each block and O columns
+        // [64 hf, 64 hf + 64). The pair (same quarter) exchanges through shared memory and meets
+        // at mbarrier xbar[quarter] (bounded waits, so an abort cannot leave one warp waiting).
         const int      qq    = warp & 3;
+        const int      hf    = (warp - 2) >> 2;
         const int      row   = qq * 32 + lane;
         const int      iq    = q0 + row;  // query index within the sequence
         const uint32_t lanes = (uint32_t) (qq * 32) << 16;
+        float *        xm    = xchg;  // [2 parity][2 halves][128 rows]
         float          m = -INFINITY, l = 0.0f;
         bool           ok = true;
+        auto pair_xchg = [&](int phase) -> bool {
+            __syncwarp();
+            if (lane == 0) {
+                ptx::mbar_arrive(&xbar[qq]);
+            }
+            return __all_sync(0xffffffffu, tc_wait(&xbar[qq], phase & 1, &abort_flag, a.err));
+        };
         for (int i = 0; i < nblk; i++) {
-            // every exit is warp-uniform: tcgen05.ld / st below are warp-collective
+            // every exit is warp-uniform (tcgen05.ld / st are warp-collective) and pair-uniform
+            // (both warps of a pair see the same barrier phases and the same abort flag)
             if (!__all_sync(0xffffffffu, tc_wait(&s_full[i & 1], (i >> 1) & 1, &abort_flag, a.err))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            uint32_t r[64];
-            tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK), r);
-            tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK + 32), r + 32);
-            const int key0 = (kb_lo + i) * kTcBK;
+            uint32_t r[32];
+            tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK + hf * 32), r);
+            const int key0 = (kb_lo + i) * kTcBK + hf * 32;
             // the mask, only on a block that crosses a boundary for this row
-            bool need = key0 + kTcBK > a.Skv;
+            bool need = key0 + 32 > a.Skv;
             if (MASK == TC_MASK_CAUSAL) {
-                need = need || key0 + kTcBK - 1 > iq + a.causal_off;
+                need = need || key0 + 31 > iq + a.causal_off;
             } else if (MASK == TC_MASK_WINDOW) {
-                need = need || key0 < iq - a.window || key0 + kTcBK - 1 > iq + a.window;
+                need = need || key0 < iq - a.window || key0 + 31 > iq + a.window;
             }
             if (need) {
 #pragma unroll
-                for (int c = 0; c < kTcBK; c++) {
+                for (int c = 0; c < 32; c++) {
                     const int j  = key0 + c;
                     bool      in = j < a.Skv;
                     if (MASK == TC_MASK_CAUSAL) {
@@ -288,12 +307,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     }
                 }
             }
-            float mx = -INFINITY;
+            float mt[8];
 #pragma unroll
-            for (int c = 0; c < kTcBK; c++) {
-                mx = fmaxf(mx, __uint_as_float(r[c]));
+            for (int c = 0; c < 8; c++) {
+                mt[c] = fmaxf(fmaxf(__uint_as_float(r[c]), __uint_as_float(r[c + 8])),
+                              fmaxf(__uint_as_float(r[c + 16]), __uint_as_float(r[c + 24])));
             }
-            // running reference max (log2 domain); moves only when exceeded by > 2^kRescaleLog2
+            const float mh = fmaxf(fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3])),
+                                   fmaxf(fmaxf(mt[4], mt[5]), fmaxf(mt[6], mt[7])));
+            // the row's block max from both halves (double-buffered by block parity)
+            xm[((i & 1) * 2 + hf) * 128 + row] = mh;
+            if (!pair_xchg(i)) {
+                ok = false;
+                break;
+            }
+            const float mx = fmaxf(mh, xm[((i & 1) * 2 + (hf ^ 1)) * 128 + row]);
+            // running reference max (log2 domain); moves only when exceeded by > 2^kRescaleLog2.
+            // Both threads of a row apply the same rule to the same values.
             const float mb    = mx * a.scale_log2;
             float       alpha = 1.0f;
             bool        resc  = false;
@@ -305,13 +335,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 resc  = true;
             }
             const float nm = -m;
-            float       ls = 0.0f;
+            float       ps[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
 #pragma unroll
-            for (int c = 0; c < kTcBK; c++) {
+            for (int c = 0; c < 32; c++) {
                 const float p = m == -INFINITY ? 0.0f : ex2_fast(fmaf(__uint_as_float(r[c]), a.scale_log2, nm));
                 r[c]          = __float_as_uint(p);
-                ls += p;
+                ps[c & 3] += p;
             }
+            const float ls = (ps[0] + ps[1]) + (ps[2] + ps[3]);
             if (i > 0) {
                 // the previous P.V has finished: O may be rescaled and P overwritten
                 if (!__all_sync(0xffffffffu, tc_wait(pv_done, (i - 1) & 1, &abort_flag, a.err))) {
@@ -321,32 +352,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-                    for (int c = 0; c < kTcD / 32; c++) {
+                    for (int c = 0; c < 2; c++) {
                         uint32_t o[32];
-                        tmem_ld32(tO + lanes + (uint32_t) (c * 32), o);
+                        const uint32_t col = (uint32_t) (hf * 64 + c * 32);
+                        tmem_ld32(tO + lanes + col, o);
 #pragma unroll
                         for (int e = 0; e < 32; e++) {
                             o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
                         }
-                        tmem_st32(tO + lanes + (uint32_t) (c * 32), o);
+                        tmem_st32(tO + lanes + col, o);
                     }
                 }
             }
             l = l * alpha + ls;
-            // P row into the swizzled [128][64] operand tile(s): 16-byte unit u of row `row` goes to
-            // unit u ^ (row % 8) (128-byte swizzle, rows 128 bytes apart)
+            // this half's P columns into the swizzled [128][64] operand tile(s): 16-byte unit u of
+            // row `row` goes to unit u ^ (row % 8) (128-byte swizzle, rows 128 bytes apart)
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                uint32_t hi[4], lo[4];
+            for (int uu = 0; uu < 4; uu++) {
+                const int u = hf * 4 + uu;
+                uint32_t  hi[4], lo[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float  p0 = __uint_as_float(r[u * 8 + 2 * e]), p1 = __uint_as_float(r[u * 8 + 2 * e + 1]);
-                    const __half h0 = __float2half_rn(p0), h1 = __float2half_rn(p1);
-                    __half2      hh = __halves2half2(h0, h1);
-                    hi[e]           = *reinterpret_cast<uint32_t *>(&hh);
+                    const float  p0 = __uint_as_float(r[uu * 8 + 2 * e]), p1 = __uint_as_float(r[uu * 8 + 2 * e + 1]);
+                    const __half2 hh = __floats2half2_rn(p0, p1);
+                    hi[e]            = *reinterpret_cast<const uint32_t *>(&hh);
                     if (SPLIT) {
-                        __half2 ll = __floats2half2_rn(p0 - __half2float(h0), p1 - __half2float(h1));
-                        lo[e]      = *reinterpret_cast<uint32_t *>(&ll);
+                        const float2  hf2 = __half22float2(hh);
+                        const __half2 ll  = __floats2half2_rn(p0 - hf2.x, p1 - hf2.y);
+                        lo[e]             = *reinterpret_cast<const uint32_t *>(&ll);
                     }
                 }
                 const int off = row * 128 + ((u ^ (row & 7)) << 4);
@@ -366,12 +399,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = __all_sync(0xffffffffu, tc_wait(pv_done, (nblk - 1) & 1, &abort_flag, a.err));
             tc_fence_after();
         }
-        const float inv = (ok && l > 0.0f) ? 1.0f / l : 0.0f;
+        // row sum of both halves (block parity nblk & 1 is free: the last exchange used the other)
+        xm[((nblk & 1) * 2 + hf) * 128 + row] = l;
+        if (ok) {
+            ok = pair_xchg(nblk);
+        }
+        const float lt  = ok ? l + xm[((nblk & 1) * 2 + (hf ^ 1)) * 128 + row] : 0.0f;
+        const float inv = (ok && lt > 0.0f) ? 1.0f / lt : 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < kTcD / 32; c++) {
-            uint32_t o[32];
+        for (int c = 0; c < 2; c++) {
+            const int col = hf * 64 + c * 32;
+            uint32_t  o[32];
             if (nblk > 0 && ok) {
-                tmem_ld32(tO + lanes + (uint32_t) (c * 32), o);
+                tmem_ld32(tO + lanes + (uint32_t) col, o);
             } else {
 #pragma unroll
                 for (int e = 0; e < 32; e++) {
@@ -379,7 +419,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             if (iq < a.Sq) {
-                const int64_t base = ((int64_t) b * a.Sq + iq) * a.o_ts + (int64_t) h * kTcD + c * 32;
+                const int64_t base = ((int64_t) b * a.Sq + iq) * a.o_ts + (int64_t) h * kTcD + col;
                 if (a.o_type == ACB_TYPE_F32) {
                     float4 * d = reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.o) + base);
 #pragma unroll
