@@ -108,7 +108,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t * xbar     = pv_done + 1;  // [4]: softmax pair exchange, one per TMEM lane quarter
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
     __shared__ volatile int abort_flag;
-    __shared__ float        xchg[2 * 2 * kTcBQ];  // softmax pair exchange: [parity][half][row]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -151,7 +150,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ptx::smem_u32(tmem_slot)),
-                     "r"(256));
+                     "r"(512));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     ptx::grid_dep_wait();
@@ -160,6 +159,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     const uint32_t tmem  = *tmem_slot;
     const uint32_t tO    = tmem + 128;  // S buffers at columns 0 and 64, O at 128..255
+    const uint32_t tX    = tmem + 256;  // softmax pair exchange: column 256 + 2 * parity + half
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
@@ -257,22 +257,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else {
         // softmax: two threads per query row. Warp w (2..9) reads TMEM lane quarter w % 4; half
         // hf = (w - 2) / 4 owns key columns [32 hf, 32 hf + 32) of each block and O columns
-        // [64 hf, 64 hf + 64). The pair (same quarter) exchanges through shared memory and meets
-        // at mbarrier xbar[quarter] (bounded waits, so an abort cannot leave one warp waiting).
+        // [64 hf, 64 hf + 64). The pair (same quarter, hence the same TMEM lanes) exchanges row
+        // values through TMEM columns 256..259 and meets at mbarrier xbar[quarter] (bounded
+        // waits, so an abort cannot leave one warp waiting).
         const int      qq    = warp & 3;
         const int      hf    = (warp - 2) >> 2;
         const int      row   = qq * 32 + lane;
         const int      iq    = q0 + row;  // query index within the sequence
         const uint32_t lanes = (uint32_t) (qq * 32) << 16;
-        float *        xm    = xchg;  // [2 parity][2 halves][128 rows]
         float          m = -INFINITY, l = 0.0f;
         bool           ok = true;
-        auto pair_xchg = [&](int phase) -> bool {
+        // publish v in this half's exchange column for `phase`, wait for the partner, return its value
+        auto pair_xchg = [&](int phase, float v, float * other) -> bool {
+            tmem_st1(tX + lanes + (uint32_t) ((phase & 1) * 2 + hf), __float_as_uint(v));
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 ptx::mbar_arrive(&xbar[qq]);
             }
-            return __all_sync(0xffffffffu, tc_wait(&xbar[qq], phase & 1, &abort_flag, a.err));
+            if (!__all_sync(0xffffffffu, tc_wait(&xbar[qq], phase & 1, &abort_flag, a.err))) {
+                return false;
+            }
+            tc_fence_after();
+            *other = __uint_as_float(tmem_ld1(tX + lanes + (uint32_t) ((phase & 1) * 2 + (hf ^ 1))));
+            return true;
         };
         for (int i = 0; i < nblk; i++) {
             // every exit is warp-uniform (tcgen05.ld / st are warp-collective) and pair-uniform
@@ -316,12 +324,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float mh = fmaxf(fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3])),
                                    fmaxf(fmaxf(mt[4], mt[5]), fmaxf(mt[6], mt[7])));
             // the row's block max from both halves (double-buffered by block parity)
-            xm[((i & 1) * 2 + hf) * 128 + row] = mh;
-            if (!pair_xchg(i)) {
+            float mo;
+            if (!pair_xchg(i, mh, &mo)) {
                 ok = false;
                 break;
             }
-            const float mx = fmaxf(mh, xm[((i & 1) * 2 + (hf ^ 1)) * 128 + row]);
+            const float mx = fmaxf(mh, mo);
             // running reference max (log2 domain); moves only when exceeded by > 2^kRescaleLog2.
             // Both threads of a row apply the same rule to the same values.
             const float mb    = mx * a.scale_log2;
@@ -399,12 +407,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = __all_sync(0xffffffffu, tc_wait(pv_done, (nblk - 1) & 1, &abort_flag, a.err));
             tc_fence_after();
         }
-        // row sum of both halves (block parity nblk & 1 is free: the last exchange used the other)
-        xm[((nblk & 1) * 2 + hf) * 128 + row] = l;
+        // row sum of both halves (exchange slot nblk & 1 is free: the last exchange used the other)
+        float lo_sum = 0.0f;
         if (ok) {
-            ok = pair_xchg(nblk);
+            ok = pair_xchg(nblk, l, &lo_sum);
         }
-        const float lt  = ok ? l + xm[((nblk & 1) * 2 + (hf ^ 1)) * 128 + row] : 0.0f;
+        const float lt  = ok ? l + lo_sum : 0.0f;
         const float inv = (ok && lt > 0.0f) ? 1.0f / lt : 0.0f;
 #pragma unroll 1
         for (int c = 0; c < 2; c++) {
@@ -454,7 +462,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     }
 }
 

@@ -87,6 +87,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t * r) {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// one 32-bit TMEM column of this warp's lane quarter (lane = thread), store / load
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+    uint32_t v;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v) : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    return v;
+}
+
 // generic-proxy shared-memory writes made visible to the tensor cores (async proxy)
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
