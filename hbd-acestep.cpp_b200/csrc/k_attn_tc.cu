@@ -3,22 +3,24 @@
 // sliding window of the even layers, 339-352 cross-attention):
 //     O[b,i,h,:] = softmax_j( Q[b,i,h,:] . K[b,j,h/G,:] * scale + mask(i,j) ) V[b,j,h/G,:]
 //
-// One CTA per (128 queries, head, batch), 6 warps:
-//   warp 0      TMA: the Q tile once, then key blocks of 64: K [64][128] and V^T [128][64] into two
-//               separate 2-3 stage rings (a K stage is released as soon as its scores are
-//               computed, a V stage after P.V), all 128-byte swizzled K-major tiles;
-//   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma: S = Q.K^T (M=128 queries,
-//               N=64 keys) into one of two S buffers, and O += P.V (M=128, N=128 head dims) into
-//               the O accumulator; S for block i+2 is issued right after P.V of block i, so the
-//               tensor cores compute the next scores while the softmax of block i+1 runs;
+// One CTA per (128 queries, head, batch), 10 warps; 512 TMEM columns hold the two S buffers, the
+// O accumulator, Q and P (the A operands of both products, two f16 per 32-bit column), so the
+// tensor cores read only K and V from shared memory:
+//   warp 0      TMA: key blocks of 64, K [64][128] and V^T [128][64], into two separate 3-4 stage
+//               rings (a K stage is released as soon as its scores are computed, a V stage after
+//               P.V), 128-byte swizzled K-major tiles;
+//   warp 1      one thread issues tcgen05.mma with A from TMEM: S = Q.K^T (M=128 queries, N=64
+//               keys) into one of two S buffers, and O += P.V (M=128, N=128 head dims); S for
+//               block i+2 is issued right after P.V of block i, so the tensor cores compute the
+//               next scores while the softmax of block i+1 runs;
 //   warps 2..9  softmax, two threads per query row (its TMEM lane; warps w and w+4 share a lane
-//               quarter and take 32 of the 64 key columns each): scores from TMEM, the mask only
-//               on blocks that cross a boundary, the block max combined by the pair through
-//               shared memory, one FFMA and one ex2 per score (scale folded into log2 e); the
-//               reference max moves (and the O row in TMEM is rescaled, each thread its 64
-//               columns) only when the block max exceeds it by more than 2^8, so P <= 256; P
-//               written as a swizzled f16 operand tile; at the end O divided by the row sum and
-//               stored.
+//               quarter): each first copies its half of the row's Q into TMEM, then per block
+//               takes 32 of the 64 key columns: scores from TMEM, the mask only on blocks that
+//               cross a boundary, the block max combined by the pair through TMEM, one FFMA and
+//               one ex2 per score (scale folded into log2 e); the reference max moves (and the
+//               O row is rescaled, each thread its 64 columns) only when the block max exceeds
+//               it by more than 2^8, so P <= 256; P stored to TMEM as f16; at the end O divided
+//               by the row sum and stored.
 // SPLIT: every operand comes as f16 hi and lo planes (hi + lo = the f32 value) and each product is
 // lo.hi + hi.lo + hi.hi, P split the same way -- f32-accurate attention (the reference CPU build's
 // qwen3_attn_f32 / dit_attn_f32). Every wait is bounded; on a timeout the kernel records
@@ -39,6 +41,9 @@ constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
 enum { TC_MASK_NONE = 0, TC_MASK_CAUSAL = 1, TC_MASK_WINDOW = 2 };
 
 struct AttnTcArgs {
+    const uint16_t * q;     // Q hi plane: element (b, i, h, d) at (b*Sq + i)*q_ts + h*128 + d
+    int64_t          q_ts;
+    int64_t          q_lo;  // lo plane offset (elements)
     void *  o;
     int     o_type;
     int64_t o_ts;  // O element (b, i, h, d) at (b*Sq + i)*o_ts + h*128 + d
@@ -49,14 +54,15 @@ struct AttnTcArgs {
 };
 
 template <bool SPLIT> struct TcLayout {
-    static constexpr int NP    = SPLIT ? 2 : 1;               // operand planes
-    static constexpr int QB    = NP * 2 * 16384;              // Q: plane x d-chunk x [128][64]
-    static constexpr int KB    = NP * 2 * 8192;               // K block: plane x d-chunk x [64][64]
-    static constexpr int VB    = NP * 16384;                  // V^T block: plane x [128][64]
-    static constexpr int NK    = SPLIT ? 2 : 3;               // K ring stages
-    static constexpr int NV    = SPLIT ? 2 : 3;               // V ring stages
-    static constexpr int PB    = NP * 16384;                  // P: plane x [128][64]
-    static constexpr int TOTAL = QB + NK * KB + NV * VB + PB;  // 224 KB split, 144 KB otherwise
+    static constexpr int NP    = SPLIT ? 2 : 1;       // operand planes
+    static constexpr int KB    = NP * 2 * 8192;       // K block: plane x d-chunk x [64][64]
+    static constexpr int VB    = NP * 16384;          // V^T block: plane x [128][64]
+    static constexpr int NK    = SPLIT ? 3 : 4;       // K ring stages
+    static constexpr int NV    = SPLIT ? 3 : 4;       // V ring stages
+    static constexpr int TOTAL = NK * KB + NV * VB;   // 192 KB split, 128 KB otherwise
+    // TMEM columns (512 allocated): S buffers 0 and 64, O 128..255, Q planes (64 columns each:
+    // two f16 per column), P planes (32 columns each), the softmax pair exchange
+    static constexpr uint32_t TQ = 256, TP = TQ + NP * 64, TX = TP + NP * 32;
 };
 
 // 2^x on the special-function unit (relative error ~2^-22; -inf -> +0, denormal results flush to 0)
@@ -84,20 +90,34 @@ __device__ __forceinline__ bool tc_wait(uint64_t * bar, uint32_t parity, volatil
     return true;
 }
 
+// D (TMEM) += A (TMEM: lane = row, two f16 of K per 32-bit column) x B (shared-memory descriptor)
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t * r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 template <int MASK, bool SPLIT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mql,
-                   const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mkl,
+    attn_tc_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mkl,
                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mvl,
                    const AttnTcArgs a) {
     using Lay = TcLayout<SPLIT>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t * smem   = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t * sQ     = smem;
-    uint8_t * sK     = smem + Lay::QB;
-    uint8_t * sV     = sK + Lay::NK * Lay::KB;
-    uint8_t * sP     = sV + Lay::NV * Lay::VB;
-    uint64_t * q_full   = reinterpret_cast<uint64_t *>(sP + Lay::PB);
+    uint8_t * smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t * sK   = smem;
+    uint8_t * sV   = sK + Lay::NK * Lay::KB;
+    uint64_t * q_full   = reinterpret_cast<uint64_t *>(sV + Lay::NV * Lay::VB);
     uint64_t * k_full   = q_full + 1;
     uint64_t * k_empty  = k_full + Lay::NK;
     uint64_t * v_full   = k_empty + Lay::NK;
@@ -127,7 +147,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
-        ptx::mbar_init(q_full, 1);
+        ptx::mbar_init(q_full, 8);  // one arrival per softmax warp once its Q columns are in TMEM
         for (int s = 0; s < Lay::NK; s++) {
             ptx::mbar_init(&k_full[s], 1);
             ptx::mbar_init(&k_empty[s], 1);
@@ -144,7 +164,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ptx::mbar_init(&xbar[x], 2);  // the two warps of a pair
         }
         ptx::fence_mbar_init();
-        tma_prefetch_desc(&mq);
         tma_prefetch_desc(&mk);
         tma_prefetch_desc(&mv);
     }
@@ -157,18 +176,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem  = *tmem_slot;
-    const uint32_t tO    = tmem + 128;  // S buffers at columns 0 and 64, O at 128..255
-    const uint32_t tX    = tmem + 256;  // softmax pair exchange: column 256 + 2 * parity + half
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tO   = tmem + 128;
+    const uint32_t tQ   = tmem + Lay::TQ;
+    const uint32_t tP   = tmem + Lay::TP;
+    const uint32_t tX   = tmem + Lay::TX;
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
-            ptx::mbar_arrive_expect_tx(q_full, Lay::QB);
-            for (int p = 0; p < Lay::NP; p++) {
-                for (int c = 0; c < 2; c++) {
-                    tma_load_2d(sQ + (p * 2 + c) * 16384, p ? &mql : &mq, h * kTcD + c * 64, b * a.Sq + q0, q_full);
-                }
-            }
             for (int i = 0; i < nblk; i++) {
                 const int key0 = (kb_lo + i) * kTcBK;
                 const int sk = i % Lay::NK, sv = i % Lay::NV;
@@ -195,10 +210,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else if (warp == 1) {
         if (lane == 0 && nblk > 0 && tc_wait(q_full, 0, &abort_flag, a.err)) {
+            tc_fence_after();
             constexpr uint32_t idesc_s = idesc_kind_f16(128, kTcBK, true);
             constexpr uint32_t idesc_o = idesc_kind_f16(128, kTcD, true);
-            const uint32_t     q_addr  = ptx::smem_u32(sQ);
-            const uint32_t     p_addr  = ptx::smem_u32(sP);
             // products (A plane, B plane): lo.hi + hi.lo + hi.hi (small terms first), or hi.hi
             constexpr int      n_prod = SPLIT ? 3 : 1;
             const int          pa[3]  = { SPLIT ? 1 : 0, 0, 0 };
@@ -217,8 +231,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     for (int kk = 0; kk < kTcD / 16; kk++) {
                         const int      c   = kk >> 2;
                         const uint32_t off = (uint32_t) ((kk & 3) * 32);
-                        umma_f16kind(tS, smem_desc_sw128(q_addr + (pa[pr] * 2 + c) * 16384 + off),
-                                     smem_desc_sw128(st + (pb[pr] * 2 + c) * 8192 + off), idesc_s, acc);
+                        umma_ts(tS, tQ + (uint32_t) (pa[pr] * 64 + kk * 8),
+                                smem_desc_sw128(st + (pb[pr] * 2 + c) * 8192 + off), idesc_s, acc);
                         acc = 1;
                     }
                 }
@@ -241,9 +255,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int pr = 0; pr < n_prod; pr++) {
 #pragma unroll
                     for (int kk = 0; kk < kTcBK / 16; kk++) {
-                        const uint32_t off = (uint32_t) (kk * 32);
-                        umma_f16kind(tO, smem_desc_sw128(p_addr + pa[pr] * 16384 + off),
-                                     smem_desc_sw128(vt + pb[pr] * 16384 + off), idesc_o, acc);
+                        umma_ts(tO, tP + (uint32_t) (pa[pr] * 32 + kk * 8),
+                                smem_desc_sw128(vt + pb[pr] * 16384 + (uint32_t) (kk * 32)), idesc_o, acc);
                         acc = 1;
                     }
                 }
@@ -256,10 +269,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // softmax: two threads per query row. Warp w (2..9) reads TMEM lane quarter w % 4; half
-        // hf = (w - 2) / 4 owns key columns [32 hf, 32 hf + 32) of each block and O columns
-        // [64 hf, 64 hf + 64). The pair (same quarter, hence the same TMEM lanes) exchanges row
-        // values through TMEM columns 256..259 and meets at mbarrier xbar[quarter] (bounded
-        // waits, so an abort cannot leave one warp waiting).
+        // hf = (w - 2) / 4 owns head dims [64 hf, 64 hf + 64) of Q and O and key columns
+        // [32 hf, 32 hf + 32) of each block. The pair (same quarter, hence the same TMEM lanes)
+        // exchanges row values through TMEM and meets at mbarrier xbar[quarter] (bounded waits,
+        // so an abort cannot leave one warp waiting).
         const int      qq    = warp & 3;
         const int      hf    = (warp - 2) >> 2;
         const int      row   = qq * 32 + lane;
@@ -267,6 +280,36 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t lanes = (uint32_t) (qq * 32) << 16;
         float          m = -INFINITY, l = 0.0f;
         bool           ok = true;
+        // this row's Q (dims [64 hf, 64 hf + 64) of each plane) into TMEM: 32 columns per plane
+        {
+            const uint16_t * qr = a.q + ((int64_t) b * a.Sq + iq) * a.q_ts + (int64_t) h * kTcD + hf * 64;
+#pragma unroll 1
+            for (int p = 0; p < Lay::NP; p++) {
+                uint32_t v[32];
+                if (iq < a.Sq) {
+                    const uint4 * src = reinterpret_cast<const uint4 *>(qr + (p ? a.q_lo : 0));
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const uint4 t = src[e];
+                        v[4 * e]      = t.x;
+                        v[4 * e + 1]  = t.y;
+                        v[4 * e + 2]  = t.z;
+                        v[4 * e + 3]  = t.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        v[e] = 0u;
+                    }
+                }
+                tmem_st32(tQ + lanes + (uint32_t) (p * 64 + hf * 32), v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                ptx::mbar_arrive(q_full);
+            }
+        }
         // publish v in this half's exchange column for `phase`, wait for the partner, return its value
         auto pair_xchg = [&](int phase, float v, float * other) -> bool {
             tmem_st1(tX + lanes + (uint32_t) ((phase & 1) * 2 + hf), __float_as_uint(v));
@@ -284,7 +327,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
         for (int i = 0; i < nblk; i++) {
             // every exit is warp-uniform (tcgen05.ld / st are warp-collective) and pair-uniform
-            // (both warps of a pair see the same barrier phases and the same abort flag)
             if (!__all_sync(0xffffffffu, tc_wait(&s_full[i & 1], (i >> 1) & 1, &abort_flag, a.err))) {
                 ok = false;
                 break;
@@ -323,16 +365,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             const float mh = fmaxf(fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3])),
                                    fmaxf(fmaxf(mt[4], mt[5]), fmaxf(mt[6], mt[7])));
-            // the row's block max from both halves (double-buffered by block parity)
             float mo;
             if (!pair_xchg(i, mh, &mo)) {
                 ok = false;
                 break;
             }
-            const float mx = fmaxf(mh, mo);
             // running reference max (log2 domain); moves only when exceeded by > 2^kRescaleLog2.
             // Both threads of a row apply the same rule to the same values.
-            const float mb    = mx * a.scale_log2;
+            const float mb    = fmaxf(mh, mo) * a.scale_log2;
             float       alpha = 1.0f;
             bool        resc  = false;
             if (m == -INFINITY) {
@@ -351,6 +391,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ps[c & 3] += p;
             }
             const float ls = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+            // P of this half as f16 pairs (hi, and lo = f16(p - hi) when split)
+            uint32_t ph[16], pl[16];
+#pragma unroll
+            for (int e = 0; e < 16; e++) {
+                const float   p0 = __uint_as_float(r[2 * e]), p1 = __uint_as_float(r[2 * e + 1]);
+                const __half2 hh = __floats2half2_rn(p0, p1);
+                ph[e]            = *reinterpret_cast<const uint32_t *>(&hh);
+                if (SPLIT) {
+                    const float2  f2 = __half22float2(hh);
+                    const __half2 ll = __floats2half2_rn(p0 - f2.x, p1 - f2.y);
+                    pl[e]            = *reinterpret_cast<const uint32_t *>(&ll);
+                }
+            }
             if (i > 0) {
                 // the previous P.V has finished: O may be rescaled and P overwritten
                 if (!__all_sync(0xffffffffu, tc_wait(pv_done, (i - 1) & 1, &abort_flag, a.err))) {
@@ -361,7 +414,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
                     for (int c = 0; c < 2; c++) {
-                        uint32_t o[32];
+                        uint32_t       o[32];
                         const uint32_t col = (uint32_t) (hf * 64 + c * 32);
                         tmem_ld32(tO + lanes + col, o);
 #pragma unroll
@@ -373,30 +426,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             l = l * alpha + ls;
-            // this half's P columns into the swizzled [128][64] operand tile(s): 16-byte unit u of
-            // row `row` goes to unit u ^ (row % 8) (128-byte swizzle, rows 128 bytes apart)
-#pragma unroll
-            for (int uu = 0; uu < 4; uu++) {
-                const int u = hf * 4 + uu;
-                uint32_t  hi[4], lo[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float  p0 = __uint_as_float(r[uu * 8 + 2 * e]), p1 = __uint_as_float(r[uu * 8 + 2 * e + 1]);
-                    const __half2 hh = __floats2half2_rn(p0, p1);
-                    hi[e]            = *reinterpret_cast<const uint32_t *>(&hh);
-                    if (SPLIT) {
-                        const float2  hf2 = __half22float2(hh);
-                        const __half2 ll  = __floats2half2_rn(p0 - hf2.x, p1 - hf2.y);
-                        lo[e]             = *reinterpret_cast<const uint32_t *>(&ll);
-                    }
-                }
-                const int off = row * 128 + ((u ^ (row & 7)) << 4);
-                *reinterpret_cast<uint4 *>(sP + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                if (SPLIT) {
-                    *reinterpret_cast<uint4 *>(sP + 16384 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                }
+            tmem_st16(tP + lanes + (uint32_t) (hf * 16), ph);
+            if (SPLIT) {
+                tmem_st16(tP + lanes + (uint32_t) (32 + hf * 16), pl);
             }
-            fence_proxy_async_smem();
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -547,17 +581,14 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     const uint16_t * q16 = reinterpret_cast<const uint16_t *>(q);
     const uint16_t * k16 = reinterpret_cast<const uint16_t *>(k);
     const uint16_t * v16 = reinterpret_cast<const uint16_t *>(vt);
-    CUtensorMap      mq, mql, mk, mkl, mv, mvl;
-    const int64_t    qc = (int64_t) Nh * kTcD, kc = (int64_t) Nkv * kTcD;
-    bool ok = make_map_2d(&mq, q16, true, qc, (int64_t) batch * Sq, q_ts, 64, kTcBQ) &&
-              make_map_2d(&mk, k16, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
+    CUtensorMap      mk, mkl, mv, mvl;
+    const int64_t    kc = (int64_t) Nkv * kTcD;
+    bool ok = make_map_2d(&mk, k16, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
               make_map_2d(&mv, v16, true, Skv, (int64_t) batch * Nkv * kTcD, vt_ld, 64, kTcD);
     if (split) {
-        ok = ok && make_map_2d(&mql, q16 + q_lo, true, qc, (int64_t) batch * Sq, q_ts, 64, kTcBQ) &&
-             make_map_2d(&mkl, k16 + k_lo, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
+        ok = ok && make_map_2d(&mkl, k16 + k_lo, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
              make_map_2d(&mvl, v16 + vt_lo, true, Skv, (int64_t) batch * Nkv * kTcD, vt_ld, 64, kTcD);
     } else {
-        mql = mq;
         mkl = mk;
         mvl = mv;
     }
@@ -565,6 +596,9 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
         return ACB_ERR_CUDA;
     }
     AttnTcArgs a = {};
+    a.q          = q16;
+    a.q_ts       = q_ts;
+    a.q_lo       = q_lo;
     a.o          = o;
     a.o_type     = o_type;
     a.o_ts       = o_ts;
@@ -577,8 +611,8 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     a.scale_log2 = scale * 1.4426950408889634f;
     a.err        = err_flag;
     const size_t smem = (size_t) (split ? TcLayout<true>::TOTAL : TcLayout<false>::TOTAL) + 1024 + 256;
-    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
-                 const CUtensorMap, const AttnTcArgs) = nullptr;
+    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const AttnTcArgs) =
+        nullptr;
 #define ACB_TC_PICK(M) kern = split ? attn_tc_kernel<M, true> : attn_tc_kernel<M, false>
     if (mask == TC_MASK_CAUSAL) {
         ACB_TC_PICK(TC_MASK_CAUSAL);
@@ -599,7 +633,7 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = (flags & ACB_FLAG_PDL) ? attr : nullptr;
     cfg.numAttrs                                       = (flags & ACB_FLAG_PDL) ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mq, mql, mk, mkl, mv, mvl, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mkl, mv, mvl, a);
     if (e != cudaSuccess) {
         set_last_cuda_error(e);
         return ACB_ERR_CUDA;
