@@ -3,24 +3,25 @@
 // sliding window of the even layers, 339-352 cross-attention):
 //     O[b,i,h,:] = softmax_j( Q[b,i,h,:] . K[b,j,h/G,:] * scale + mask(i,j) ) V[b,j,h/G,:]
 //
-// One CTA per (128 queries, head, batch), 10 warps; 512 TMEM columns hold the two S buffers, the
-// O accumulator, Q and P (the A operands of both products, two f16 per 32-bit column), so the
-// tensor cores read only K and V from shared memory:
-//   warp 0      TMA: key blocks of 64, K [64][128] and V^T [128][64], into two separate 3-4 stage
-//               rings (a K stage is released as soon as its scores are computed, a V stage after
-//               P.V), 128-byte swizzled K-major tiles;
-//   warp 1      one thread issues tcgen05.mma with A from TMEM: S = Q.K^T (M=128 queries, N=64
-//               keys) into one of two S buffers, and O += P.V (M=128, N=128 head dims); S for
-//               block i+2 is issued right after P.V of block i, so the tensor cores compute the
-//               next scores while the softmax of block i+1 runs;
+// One CTA per (128 queries, head, batch), 10 warps; the 512 TMEM columns hold two S/P buffers, the
+// O accumulator and Q (P and Q are the A operands of the two products, two f16 per 32-bit column),
+// so the tensor cores read only K and V from shared memory, and every MMA is N = 128 wide (the
+// narrower N = 64 form runs at about two thirds of the tensor rate):
+//   warp 0      TMA: key blocks of 128, K [128][128] and V^T [128][128], into separate rings (a K
+//               stage is released as soon as its scores are computed, a V stage after P.V),
+//               128-byte swizzled K-major tiles;
+//   warp 1      one thread issues tcgen05.mma with A from TMEM: S = Q.K^T (M=128 queries, N=128
+//               keys) into one of the two S/P buffers, and O += P.V (M=128, N=128 head dims); S for
+//               block i+2 is issued right after P.V of block i (the tensor pipe runs them in order,
+//               so S(i+2) overwrites the P(i) it aliases only after P.V(i) has read it);
 //   warps 2..9  softmax, two threads per query row (its TMEM lane; warps w and w+4 share a lane
 //               quarter): each first copies its half of the row's Q into TMEM, then per block
-//               takes 32 of the 64 key columns: scores from TMEM, the mask only on blocks that
-//               cross a boundary, the block max combined by the pair through TMEM, one FFMA and
-//               one ex2 per score (scale folded into log2 e); the reference max moves (and the
-//               O row is rescaled, each thread its 64 columns) only when the block max exceeds
-//               it by more than 2^8, so P <= 256; P stored to TMEM as f16; at the end O divided
-//               by the row sum and stored.
+//               takes 64 of the 128 key columns: scores from TMEM, the mask only on blocks that
+//               cross a boundary, the block max combined by the pair through shared memory, one
+//               FFMA and one ex2 per score (scale folded into log2 e); the reference max moves
+//               (and the O row is rescaled, each thread its 64 columns) only when the block max
+//               exceeds it by more than 2^8, so P <= 256; P written over the block's S as f16; at
+//               the end O divided by the row sum and stored.
 // SPLIT: every operand comes as f16 hi and lo planes (hi + lo = the f32 value) and each product is
 // lo.hi + hi.lo + hi.hi, P split the same way -- f32-accurate attention (the reference CPU build's
 // qwen3_attn_f32 / dit_attn_f32). Every wait is bounded; on a timeout the kernel records
@@ -34,7 +35,7 @@
 namespace acb {
 
 constexpr int kTcBQ      = 128;  // queries per CTA = TMEM lanes
-constexpr int kTcBK      = 64;   // keys per block
+constexpr int kTcBK      = 128;  // keys per block
 constexpr int kTcD       = 128;  // head dim
 constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
 
@@ -55,14 +56,15 @@ struct AttnTcArgs {
 
 template <bool SPLIT> struct TcLayout {
     static constexpr int NP    = SPLIT ? 2 : 1;       // operand planes
-    static constexpr int KB    = NP * 2 * 8192;       // K block: plane x d-chunk x [64][64]
-    static constexpr int VB    = NP * 16384;          // V^T block: plane x [128][64]
-    static constexpr int NK    = SPLIT ? 3 : 4;       // K ring stages
-    static constexpr int NV    = SPLIT ? 3 : 4;       // V ring stages
-    static constexpr int TOTAL = NK * KB + NV * VB;   // 192 KB split, 128 KB otherwise
-    // TMEM columns (512 allocated): S buffers 0 and 64, O 128..255, Q planes (64 columns each:
-    // two f16 per column), P planes (32 columns each), the softmax pair exchange
-    static constexpr uint32_t TQ = 256, TP = TQ + NP * 64, TX = TP + NP * 32;
+    static constexpr int KB    = NP * 2 * 16384;      // K block: plane x d-chunk x [128 keys][64 d]
+    static constexpr int VB    = NP * 2 * 16384;      // V^T block: plane x key-chunk x [128 d][64 keys]
+    static constexpr int NK    = SPLIT ? 2 : 3;       // K ring stages
+    static constexpr int NV    = SPLIT ? 1 : 2;       // V ring stages
+    static constexpr int TOTAL = NK * KB + NV * VB;   // 192 KB split, 160 KB otherwise
+    // TMEM columns (512 allocated): two S/P buffers of 128 columns (S fp32; after the softmax, P
+    // as f16 pairs: hi plane in the first 64 columns, lo plane in the next 64), O at 256..383,
+    // Q planes (64 columns each: two f16 per column) from 384
+    static constexpr uint32_t TO = 256, TQ = 384;
 };
 
 // 2^x on the special-function unit (relative error ~2^-22; -inf -> +0, denormal results flush to 0)
@@ -128,6 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t * xbar     = pv_done + 1;  // [4]: softmax pair exchange, one per TMEM lane quarter
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
     __shared__ volatile int abort_flag;
+    __shared__ float        xchg[2 * 2 * kTcBQ];  // softmax pair exchange: [parity][half][row]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -177,10 +180,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t tO   = tmem + 128;
+    const uint32_t tO   = tmem + Lay::TO;
     const uint32_t tQ   = tmem + Lay::TQ;
-    const uint32_t tP   = tmem + Lay::TP;
-    const uint32_t tX   = tmem + Lay::TX;
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ptx::mbar_arrive_expect_tx(&k_full[sk], Lay::KB);
                 for (int p = 0; p < Lay::NP; p++) {
                     for (int c = 0; c < 2; c++) {
-                        tma_load_2d(kst + (p * 2 + c) * 8192, p ? &mkl : &mk, hk * kTcD + c * 64, b * a.Skv + key0,
+                        tma_load_2d(kst + (p * 2 + c) * 16384, p ? &mkl : &mk, hk * kTcD + c * 64, b * a.Skv + key0,
                                     &k_full[sk]);
                     }
                 }
@@ -204,7 +205,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint8_t * vst = sV + sv * Lay::VB;
                 ptx::mbar_arrive_expect_tx(&v_full[sv], Lay::VB);
                 for (int p = 0; p < Lay::NP; p++) {
-                    tma_load_2d(vst + p * 16384, p ? &mvl : &mv, key0, (b * a.Nkv + hk) * kTcD, &v_full[sv]);
+                    for (int c = 0; c < 2; c++) {
+                        tma_load_2d(vst + (p * 2 + c) * 16384, p ? &mvl : &mv, key0 + c * 64, (b * a.Nkv + hk) * kTcD,
+                                    &v_full[sv]);
+                    }
                 }
             }
         }
@@ -224,7 +228,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t st  = ptx::smem_u32(sK + sk * Lay::KB);
-                const uint32_t tS  = tmem + (uint32_t) ((i & 1) * kTcBK);
+                const uint32_t tS  = tmem + (uint32_t) ((i & 1) * 128);
                 uint32_t       acc = 0;
                 for (int pr = 0; pr < n_prod; pr++) {
 #pragma unroll
@@ -232,7 +236,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const int      c   = kk >> 2;
                         const uint32_t off = (uint32_t) ((kk & 3) * 32);
                         umma_ts(tS, tQ + (uint32_t) (pa[pr] * 64 + kk * 8),
-                                smem_desc_sw128(st + (pb[pr] * 2 + c) * 8192 + off), idesc_s, acc);
+                                smem_desc_sw128(st + (pb[pr] * 2 + c) * 16384 + off), idesc_s, acc);
                         acc = 1;
                     }
                 }
@@ -251,12 +255,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t vt  = ptx::smem_u32(sV + sv * Lay::VB);
+                const uint32_t tP  = tmem + (uint32_t) ((i & 1) * 128);  // P aliases this block's S buffer
                 uint32_t       acc = i > 0 ? 1u : 0u;
                 for (int pr = 0; pr < n_prod; pr++) {
 #pragma unroll
                     for (int kk = 0; kk < kTcBK / 16; kk++) {
-                        umma_ts(tO, tP + (uint32_t) (pa[pr] * 32 + kk * 8),
-                                smem_desc_sw128(vt + pb[pr] * 16384 + (uint32_t) (kk * 32)), idesc_o, acc);
+                        const int      c   = kk >> 2;
+                        const uint32_t off = (uint32_t) ((kk & 3) * 32);
+                        umma_ts(tO, tP + (uint32_t) (pa[pr] * 64 + kk * 8),
+                                smem_desc_sw128(vt + (pb[pr] * 2 + c) * 16384 + off), idesc_o, acc);
                         acc = 1;
                     }
                 }
@@ -310,10 +317,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ptx::mbar_arrive(q_full);
             }
         }
-        // publish v in this half's exchange column for `phase`, wait for the partner, return its value
+        // publish v for `phase`, wait for the partner (bounded), return its value
         auto pair_xchg = [&](int phase, float v, float * other) -> bool {
-            tmem_st1(tX + lanes + (uint32_t) ((phase & 1) * 2 + hf), __float_as_uint(v));
-            tc_fence_before();
+            xchg[((phase & 1) * 2 + hf) * kTcBQ + row] = v;
             __syncwarp();
             if (lane == 0) {
                 ptx::mbar_arrive(&xbar[qq]);
@@ -321,8 +327,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!__all_sync(0xffffffffu, tc_wait(&xbar[qq], phase & 1, &abort_flag, a.err))) {
                 return false;
             }
-            tc_fence_after();
-            *other = __uint_as_float(tmem_ld1(tX + lanes + (uint32_t) ((phase & 1) * 2 + (hf ^ 1))));
+            *other = xchg[((phase & 1) * 2 + (hf ^ 1)) * kTcBQ + row];
             return true;
         };
         for (int i = 0; i < nblk; i++) {
@@ -332,19 +337,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 break;
             }
             tc_fence_after();
-            uint32_t r[32];
-            tmem_ld32(tmem + lanes + (uint32_t) ((i & 1) * kTcBK + hf * 32), r);
-            const int key0 = (kb_lo + i) * kTcBK + hf * 32;
+            const uint32_t tS = tmem + lanes + (uint32_t) ((i & 1) * 128);
+            uint32_t       r[64];
+            tmem_ld32(tS + (uint32_t) (hf * 64), r);
+            tmem_ld32(tS + (uint32_t) (hf * 64 + 32), r + 32);
+            const int key0 = (kb_lo + i) * kTcBK + hf * 64;
             // the mask, only on a block that crosses a boundary for this row
-            bool need = key0 + 32 > a.Skv;
+            bool need = key0 + 64 > a.Skv;
             if (MASK == TC_MASK_CAUSAL) {
-                need = need || key0 + 31 > iq + a.causal_off;
+                need = need || key0 + 63 > iq + a.causal_off;
             } else if (MASK == TC_MASK_WINDOW) {
-                need = need || key0 < iq - a.window || key0 + 31 > iq + a.window;
+                need = need || key0 < iq - a.window || key0 + 63 > iq + a.window;
             }
             if (need) {
 #pragma unroll
-                for (int c = 0; c < 32; c++) {
+                for (int c = 0; c < 64; c++) {
                     const int j  = key0 + c;
                     bool      in = j < a.Skv;
                     if (MASK == TC_MASK_CAUSAL) {
@@ -360,11 +367,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             float mt[8];
 #pragma unroll
             for (int c = 0; c < 8; c++) {
-                mt[c] = fmaxf(fmaxf(__uint_as_float(r[c]), __uint_as_float(r[c + 8])),
-                              fmaxf(__uint_as_float(r[c + 16]), __uint_as_float(r[c + 24])));
+                mt[c] = fmaxf(fmaxf(fmaxf(__uint_as_float(r[c]), __uint_as_float(r[c + 8])),
+                                    fmaxf(__uint_as_float(r[c + 16]), __uint_as_float(r[c + 24]))),
+                              fmaxf(fmaxf(__uint_as_float(r[c + 32]), __uint_as_float(r[c + 40])),
+                                    fmaxf(__uint_as_float(r[c + 48]), __uint_as_float(r[c + 56]))));
             }
             const float mh = fmaxf(fmaxf(fmaxf(mt[0], mt[1]), fmaxf(mt[2], mt[3])),
                                    fmaxf(fmaxf(mt[4], mt[5]), fmaxf(mt[6], mt[7])));
+            // the pair exchange also orders both threads' reads of this S buffer before either
+            // overwrites it with P
             float mo;
             if (!pair_xchg(i, mh, &mo)) {
                 ok = false;
@@ -385,27 +396,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float nm = -m;
             float       ps[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
+            for (int c = 0; c < 64; c++) {
                 const float p = m == -INFINITY ? 0.0f : ex2_fast(fmaf(__uint_as_float(r[c]), a.scale_log2, nm));
                 r[c]          = __float_as_uint(p);
                 ps[c & 3] += p;
             }
             const float ls = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-            // P of this half as f16 pairs (hi, and lo = f16(p - hi) when split)
-            uint32_t ph[16], pl[16];
+            // P of this half as f16 pairs: hi into r[0..31], lo = f16(p - hi) into r[32..63]
 #pragma unroll
-            for (int e = 0; e < 16; e++) {
+            for (int e = 0; e < 32; e++) {
                 const float   p0 = __uint_as_float(r[2 * e]), p1 = __uint_as_float(r[2 * e + 1]);
                 const __half2 hh = __floats2half2_rn(p0, p1);
-                ph[e]            = *reinterpret_cast<const uint32_t *>(&hh);
                 if (SPLIT) {
                     const float2  f2 = __half22float2(hh);
                     const __half2 ll = __floats2half2_rn(p0 - f2.x, p1 - f2.y);
-                    pl[e]            = *reinterpret_cast<const uint32_t *>(&ll);
+                    r[2 * e + 1]     = *reinterpret_cast<const uint32_t *>(&ll);  // slot 2e+1 is read above
                 }
+                r[2 * e] = *reinterpret_cast<const uint32_t *>(&hh);
+            }
+            uint32_t ph[32], pl[32];
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                ph[e] = r[2 * e];
+                pl[e] = r[2 * e + 1];
             }
             if (i > 0) {
-                // the previous P.V has finished: O may be rescaled and P overwritten
+                // the previous P.V has finished: O may be rescaled
                 if (!__all_sync(0xffffffffu, tc_wait(pv_done, (i - 1) & 1, &abort_flag, a.err))) {
                     ok = false;
                     break;
@@ -426,11 +442,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             l = l * alpha + ls;
-            tmem_st16(tP + lanes + (uint32_t) (hf * 16), ph);
+            // P into this block's S buffer: keys [64 hf, 64 hf + 64) are columns [32 hf, 32 hf + 32)
+            // of the hi plane (columns 0..63) and of the lo plane (64..127)
+            tmem_st32(tS + (uint32_t) (hf * 32), ph);
             if (SPLIT) {
-                tmem_st16(tP + lanes + (uint32_t) (32 + hf * 16), pl);
+                tmem_st32(tS + (uint32_t) (64 + hf * 32), pl);
             }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
