@@ -22,7 +22,6 @@
 // still frees its TMEM (both CTAs of a pair meet at a cluster barrier first).
 #include <cuda.h>
 
-#include <algorithm>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -66,41 +65,7 @@ struct GemmArgs {
     int           splits;  // split-K factor; > 1: raw partials to ws, epilogue by splitk_reduce_kernel
     int           kps;     // k-tiles per split
     float *       ws;      // [splits][M][N] f32 partial accumulators
-    // tail split (wave quantisation): work units [0, full_tiles) are whole tiles; the remaining
-    // tail_rem tiles are split along K into tail_splits units each. Each split stores its raw
-    // tile to tail_ws; the last split of a tile to finish (per epilogue warp, counted in
-    // tail_cnt) sums all splits in split order and applies the epilogue.
-    int64_t       full_tiles;
-    int           tail_rem, tail_splits, tail_kps;
-    float *       tail_ws;   // [tail_rem][tail_splits][tile rows][256]
-    int *         tail_cnt;  // [tail_rem][2 CTA ranks][4 warps], zero at launch
 };
-
-// one work unit: output tile t over k-tiles [k0, k1); tail >= 0 for a split of a tail tile
-struct GemmUnit {
-    int64_t t;
-    int     k0, k1;
-    int     tail, split;
-};
-
-__device__ __forceinline__ GemmUnit gemm_unit(const GemmArgs & g, int64_t w, int64_t tiles, int k_tiles) {
-    GemmUnit u;
-    if (g.tail_rem > 0 && w >= g.full_tiles) {
-        const int64_t v = w - g.full_tiles;
-        u.tail          = (int) (v % g.tail_rem);
-        u.split         = (int) (v / g.tail_rem);
-        u.t             = g.full_tiles + u.tail;
-        u.k0            = u.split * g.tail_kps;
-        u.k1            = min(k_tiles, u.k0 + g.tail_kps);
-    } else {
-        u.t     = w % tiles;
-        u.split = (int) (w / tiles);
-        u.k0    = u.split * g.kps;
-        u.k1    = min(k_tiles, u.k0 + g.kps);
-        u.tail  = -1;
-    }
-    return u;
-}
 
 // up to 4 consecutive columns of one row: one vector access when all 4 are in range and aligned.
 // Values travel in a float4 and every index is static, so nothing is placed in local memory.
@@ -135,15 +100,6 @@ template <int T> __device__ __forceinline__ void store_cols(void * C, int64_t of
     }
 }
 
-// the same through L2 only (partials written by other CTAs of this launch)
-__device__ __forceinline__ float4 load_cols_cg(const float * src, int ncol) {
-    if (ncol == 4) {
-        return __ldcg(reinterpret_cast<const float4 *>(src));
-    }
-    return make_float4(ncol > 0 ? __ldcg(src) : 0.0f, ncol > 1 ? __ldcg(src + 1) : 0.0f, ncol > 2 ? __ldcg(src + 2) : 0.0f,
-                       ncol > 3 ? __ldcg(src + 3) : 0.0f);
-}
-
 __device__ __forceinline__ float4 load_cols(const float * src, int ncol) {
     if (ncol == 4 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
         return *reinterpret_cast<const float4 *>(src);
@@ -176,7 +132,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int64_t  n_units = PAIR ? (gridDim.x >> 1) : gridDim.x;
     const int64_t m_tiles = (g.M + Cf::kTileM - 1) / Cf::kTileM, n_tiles = (g.N + kBN - 1) / kBN;
     const int64_t tiles   = m_tiles * n_tiles;
-    const int64_t n_work  = g.tail_rem > 0 ? g.full_tiles + (int64_t) g.tail_rem * g.tail_splits : tiles * g.splits;
+    const int64_t n_work  = tiles * g.splits;
     const int     k_tiles = (int) (g.K / kBK);
 
     if (threadIdx.x == 0) {
@@ -220,11 +176,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) {
             int it = 0;  // global k-stage counter
             for (int64_t w = unit; w < n_work && !abort_flag; w += n_units) {
-                const GemmUnit u  = gemm_unit(g, w, tiles, k_tiles);
-                const int64_t  t  = u.t;
+                const int64_t t  = w % tiles;
+                const int     sp = (int) (w / tiles);
                 const int ma = (int) ((t % m_tiles) * Cf::kTileM) + (int) rank * 128;  // this CTA's A rows
                 const int nb = (int) ((t / m_tiles) * kBN) + (int) rank * Cf::kRowsB;  // this CTA's B rows
-                for (int kt = u.k0; kt < u.k1; kt++, it++) {
+                const int kt1 = min(k_tiles, (sp + 1) * g.kps);
+                for (int kt = sp * g.kps; kt < kt1; kt++, it++) {
                     const int s = it % Cf::kStages;
                     if (it >= Cf::kStages && !ptx::mbar_wait(&empty[s], ((it / Cf::kStages) - 1) & 1)) {
                         flag_timeout(g.err);
@@ -261,9 +218,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + (uint32_t) (acc * kBN);
-                const GemmUnit u      = gemm_unit(g, w, tiles, k_tiles);
-                const int      kt0    = u.k0;
-                const int      kt1    = u.k1;
+                const int      kt0    = (int) (w / tiles) * g.kps;
+                const int      kt1    = min(k_tiles, kt0 + g.kps);
                 for (int kt = kt0; kt < kt1; kt++, it++) {
                     const int s = it % Cf::kStages;
                     if (!ptx::mbar_wait(&full[s], (it / Cf::kStages) & 1)) {
@@ -318,47 +274,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 break;
             }
             tc_fence_after();
-            const GemmUnit u      = gemm_unit(g, w, tiles, k_tiles);
-            const int64_t  t      = u.t;
-            const int64_t  m_tile = (t % m_tiles) * Cf::kTileM;
-            const int64_t  m_base = m_tile + (int64_t) rank * 128 + q * 32;
-            const int64_t  n0     = (t / m_tiles) * kBN;
-            const bool     tailu  = u.tail >= 0;
-            const bool     part   = g.splits > 1 || tailu;  // raw partial accumulators
-            // partial destination: [split][M][N] (split-K) or this split's tile block (tail)
-            float * pws = tailu ? g.tail_ws + ((int64_t) (u.tail * g.tail_splits + u.split) * Cf::kTileM +
-                                               (int64_t) rank * 128 + q * 32) * kBN
-                          : (part ? g.ws + (int64_t) u.split * g.M * g.N : nullptr);
-            auto finish = [&](int64_t m, int64_t n, int ncol, float4 v) {
-                if (g.bias) {
-                    const float4 bv = load_cols(g.bias + n, ncol);
-                    v.x             = __fadd_rn(v.x, bv.x);
-                    v.y             = __fadd_rn(v.y, bv.y);
-                    v.z             = __fadd_rn(v.z, bv.z);
-                    v.w             = __fadd_rn(v.w, bv.w);
-                }
-                if (g.epi & (EPI_RES | EPI_GATED_RES)) {
-                    const float4 rv = load_cols(g.res + m * g.ldr + n, ncol);
-                    if (g.epi & EPI_GATED_RES) {
-                        const float4 gv = load_cols(g.gate + (m / g.rows_per_sample) * g.gate_stride + n, ncol);
-                        v.x             = __fmul_rn(v.x, gv.x);
-                        v.y             = __fmul_rn(v.y, gv.y);
-                        v.z             = __fmul_rn(v.z, gv.z);
-                        v.w             = __fmul_rn(v.w, gv.w);
-                    }
-                    v.x = __fadd_rn(rv.x, v.x);
-                    v.y = __fadd_rn(rv.y, v.y);
-                    v.z = __fadd_rn(rv.z, v.z);
-                    v.w = __fadd_rn(rv.w, v.w);
-                }
-                if (g.c_type == ACB_TYPE_F32) {
-                    store_cols<ACB_TYPE_F32>(g.C, m * g.ldc + n, v, ncol);
-                } else if (g.c_type == ACB_TYPE_BF16) {
-                    store_cols<ACB_TYPE_BF16>(g.C, m * g.ldc + n, v, ncol);
-                } else {
-                    store_cols<ACB_TYPE_F16>(g.C, m * g.ldc + n, v, ncol);
-                }
-            };
+            const int64_t t      = w % tiles;
+            const int64_t m_base = (t % m_tiles) * Cf::kTileM + (int64_t) rank * 128 + q * 32;
+            const int64_t n0     = (t / m_tiles) * kBN;
+            const bool    part   = g.splits > 1;  // raw partial of split w / tiles
+            float *       pws    = part ? g.ws + (w / tiles) * g.M * g.N : nullptr;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; c++) {
                 uint32_t r[32];
@@ -383,13 +303,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (m >= g.M || ncol == 0) {
                         continue;
                     }
-                    const float4 v = *reinterpret_cast<const float4 *>(stg + rr * kStgPitch + cc);
-                    if (tailu) {
-                        store_cols<ACB_TYPE_F32>(pws, (int64_t) rr * kBN + c * 32 + cc, v, ncol);
-                    } else if (part) {
+                    float4 v = *reinterpret_cast<const float4 *>(stg + rr * kStgPitch + cc);
+                    if (part) {
                         store_cols<ACB_TYPE_F32>(pws, m * g.N + n, v, ncol);
+                        continue;
+                    }
+                    if (g.bias) {
+                        const float4 bv = load_cols(g.bias + n, ncol);
+                        v.x             = __fadd_rn(v.x, bv.x);
+                        v.y             = __fadd_rn(v.y, bv.y);
+                        v.z             = __fadd_rn(v.z, bv.z);
+                        v.w             = __fadd_rn(v.w, bv.w);
+                    }
+                    if (g.epi & (EPI_RES | EPI_GATED_RES)) {
+                        const float4 rv = load_cols(g.res + m * g.ldr + n, ncol);
+                        if (g.epi & EPI_GATED_RES) {
+                            const float4 gv = load_cols(g.gate + (m / g.rows_per_sample) * g.gate_stride + n, ncol);
+                            v.x             = __fmul_rn(v.x, gv.x);
+                            v.y             = __fmul_rn(v.y, gv.y);
+                            v.z             = __fmul_rn(v.z, gv.z);
+                            v.w             = __fmul_rn(v.w, gv.w);
+                        }
+                        v.x = __fadd_rn(rv.x, v.x);
+                        v.y = __fadd_rn(rv.y, v.y);
+                        v.z = __fadd_rn(rv.z, v.z);
+                        v.w = __fadd_rn(rv.w, v.w);
+                    }
+                    if (g.c_type == ACB_TYPE_F32) {
+                        store_cols<ACB_TYPE_F32>(g.C, m * g.ldc + n, v, ncol);
+                    } else if (g.c_type == ACB_TYPE_BF16) {
+                        store_cols<ACB_TYPE_BF16>(g.C, m * g.ldc + n, v, ncol);
                     } else {
-                        finish(m, n, ncol, v);
+                        store_cols<ACB_TYPE_F16>(g.C, m * g.ldc + n, v, ncol);
                     }
                 }
                 __syncwarp();
@@ -401,50 +346,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     ptx::mbar_arrive(&tmem_empty[acc]);
                 } else {  // the pair's accumulators are handed back to the leader's MMA thread
                     mbar_arrive_cluster(mapa_shared(ptx::smem_u32(&tmem_empty[acc]), 0));
-                }
-            }
-            if (tailu && m_base < g.M) {
-                // this warp's rows of the split are stored: count it; the last of the tile's splits
-                // sums them all in split order (deterministic) and writes C. No waiting.
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    int * cnt = g.tail_cnt + ((int64_t) u.tail * 2 + rank) * 4 + q;
-                    last      = atomicAdd(cnt, 1) == g.tail_splits - 1;
-                }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-                    const float * t0 = g.tail_ws + ((int64_t) u.tail * g.tail_splits * Cf::kTileM +
-                                                    (int64_t) rank * 128 + q * 32) * kBN;
-                    const int64_t sstride = (int64_t) Cf::kTileM * kBN;  // between splits of one tile
-#pragma unroll 1
-                    for (int c = 0; c < kBN / 32; c++) {
-                        const int64_t n    = n0 + c * 32 + cc;
-                        const int     ncol = n < g.N ? (g.N - n < 4 ? (int) (g.N - n) : 4) : 0;
-                        if (ncol == 0) {
-                            continue;
-                        }
-#pragma unroll 1
-                        for (int it = 0; it < 8; it++) {
-                            const int     rr = it * 4 + sub;
-                            const int64_t m  = m_base + rr;
-                            if (m >= g.M) {
-                                continue;
-                            }
-                            const float * src = t0 + (int64_t) rr * kBN + c * 32 + cc;
-                            float4        v   = load_cols_cg(src, ncol);
-                            for (int sp = 1; sp < g.tail_splits; sp++) {
-                                const float4 b = load_cols_cg(src + sp * sstride, ncol);
-                                v.x            = __fadd_rn(v.x, b.x);
-                                v.y            = __fadd_rn(v.y, b.y);
-                                v.z            = __fadd_rn(v.z, b.z);
-                                v.w            = __fadd_rn(v.w, b.w);
-                            }
-                            finish(m, n, ncol, v);
-                        }
-                    }
                 }
             }
         }
@@ -583,63 +484,6 @@ static int pair_clusters(bool f16) {
     return c;
 }
 
-// Launch plan of one GEMM: split-K over a workspace for a few tiles, CTA pairs otherwise, and a
-// tail split when the last wave of tiles would leave many SMs idle.
-struct GemmPlan {
-    bool    pair   = false;
-    int     units  = 0;  // resident work units: CTA pairs or CTAs
-    int     splits = 1, kps = 0;
-    int64_t full_tiles = 0;
-    int     tail_rem = 0, tail_splits = 1, tail_kps = 0;
-    size_t  ws_bytes = 0;  // workspace this plan needs
-};
-
-constexpr size_t kTailCntBytes = 4096;  // counters at the start of a tail-split workspace
-
-static GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K) {
-    GemmPlan  p;
-    const int k_tiles = (int) (K / kBK);
-    p.kps             = k_tiles;
-    int kps           = 0;
-    p.splits          = choose_splits(M, N, K, &kps);
-    if (p.splits > 1) {
-        p.kps      = kps;
-        p.units    = num_sms();
-        p.ws_bytes = (size_t) p.splits * (size_t) M * (size_t) N * 4;
-        return p;
-    }
-    const int pc = M > 128 ? std::min(pair_clusters(false), pair_clusters(true)) : 0;
-    p.pair       = pc > 0;
-    p.units      = p.pair ? pc : num_sms();
-    const int     tm    = p.pair ? 256 : 128;
-    const int64_t tiles = ((M + tm - 1) / tm) * ((N + kBN - 1) / kBN);
-    const int64_t waves = tiles / p.units, rem = tiles % p.units;
-    if (waves >= 1 && rem > 0 && N % 4 == 0 && rem * 8 * 4 <= (int64_t) kTailCntBytes) {
-        // the tail tiles split S ways run ceil(rem * S / units) rounds of 1/S tile each
-        double best_t = 1.0;
-        int    best   = 1;
-        for (int S = 2; S <= 8; S++) {
-            const int kp = (k_tiles + S - 1) / S;
-            if (kp < 4 || (S - 1) * kp >= k_tiles) {
-                continue;
-            }
-            const double t = (double) ((rem * S + p.units - 1) / p.units) / S;
-            if (t < best_t - 0.05) {
-                best_t = t;
-                best   = S;
-            }
-        }
-        if (best > 1) {
-            p.full_tiles  = waves * p.units;
-            p.tail_rem    = (int) rem;
-            p.tail_splits = best;
-            p.tail_kps    = (k_tiles + best - 1) / best;
-            p.ws_bytes    = kTailCntBytes + (size_t) rem * best * tm * kBN * 4;
-        }
-    }
-    return p;
-}
-
 }  // namespace acb
 
 using namespace acb;
@@ -652,7 +496,9 @@ extern "C" size_t acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     if (M <= 0 || N <= 0 || K <= 0 || K % kBK != 0) {
         return 0;
     }
-    return plan_gemm(M, N, K).ws_bytes;
+    int       kps = 0;
+    const int sp  = choose_splits(M, N, K, &kps);
+    return sp > 1 ? (size_t) sp * (size_t) M * (size_t) N * 4 : 0;
 }
 
 extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
@@ -690,32 +536,20 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
     g.err             = err_flag;
     g.splits          = 1;
     g.kps             = (int) (K / kBK);
-    const bool     f16 = (flags & ACB_FLAG_F16) != 0;
-    const GemmPlan pl  = plan_gemm(M, N, K);
-    const bool     ws_ok = pl.ws_bytes > 0 && workspace && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 &&
-                       workspace_bytes >= pl.ws_bytes;
-    if (pl.splits > 1 && ws_ok) {
-        g.splits = pl.splits;
-        g.kps    = pl.kps;
-        g.ws     = reinterpret_cast<float *>(workspace);
-    }
-    if (pl.tail_rem > 0 && ws_ok) {
-        g.full_tiles  = pl.full_tiles;
-        g.tail_rem    = pl.tail_rem;
-        g.tail_splits = pl.tail_splits;
-        g.tail_kps    = pl.tail_kps;
-        g.tail_cnt    = reinterpret_cast<int *>(workspace);
-        g.tail_ws     = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(workspace) + kTailCntBytes);
-        // the arrival counters start at zero for every launch
-        const cudaError_t me = cudaMemsetAsync(workspace, 0, (size_t) pl.tail_rem * 8 * 4, (cudaStream_t) stream);
-        if (me != cudaSuccess) {
-            set_last_cuda_error(me);
-            return ACB_ERR_CUDA;
+    {
+        int       kps = 0;
+        const int sp  = choose_splits(M, N, K, &kps);
+        if (sp > 1 && workspace && reinterpret_cast<uintptr_t>(workspace) % 16 == 0 &&
+            workspace_bytes >= (size_t) sp * (size_t) M * (size_t) N * 4) {
+            g.splits = sp;
+            g.kps    = kps;
+            g.ws     = reinterpret_cast<float *>(workspace);
         }
     }
-    // CTA pairs when the single-CTA tiling needs no split-K (enough 256x256 tiles to fill the GPU)
-    const bool pair     = g.splits == 1 && pl.pair;
-    const int  clusters = pair ? pl.units : 0;
+    const bool f16 = (flags & ACB_FLAG_F16) != 0;
+    // CTA pairs when the single-CTA tiling needs no split (enough 256x256 tiles to fill the GPU)
+    const int  clusters = g.splits == 1 && M > 128 ? pair_clusters(f16) : 0;
+    const bool pair     = clusters > 0;
     CUtensorMap ta, tb;
     if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, N, K, ldb, pair ? 128 : kBN, f16)) {
         return ACB_ERR_CUDA;
@@ -742,14 +576,12 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
     cfg.numAttrs = na;
     cudaError_t e;
     if (pair) {
-        const int64_t work = g.tail_rem > 0 ? g.full_tiles + (int64_t) g.tail_rem * g.tail_splits
-                                            : ((M + 255) / 256) * ((N + kBN - 1) / kBN);
+        const int64_t work = ((M + 255) / 256) * ((N + kBN - 1) / kBN);
         cfg.gridDim          = dim3((unsigned) (2 * (work < clusters ? work : clusters)));
         cfg.dynamicSmemBytes = GemmCfg<true>::kSmem;
         e = cudaLaunchKernelEx(&cfg, f16 ? gemm_tc_kernel<true, true> : gemm_tc_kernel<false, true>, ta, tb, g);
     } else {
-        const int64_t work = g.tail_rem > 0 ? g.full_tiles + (int64_t) g.tail_rem * g.tail_splits
-                                            : ((M + 127) / 128) * ((N + kBN - 1) / kBN) * g.splits;
+        const int64_t work = ((M + 127) / 128) * ((N + kBN - 1) / kBN) * g.splits;
         void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
             f16 ? gemm_tc_kernel<true, false> : gemm_tc_kernel<false, false>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) GemmCfg<false>::kSmem);

@@ -162,7 +162,7 @@ acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
         int64_t Ms[3] = { (int64_t) R, (int64_t) Re, 1 };
         for (int64_t M : Ms) {
             for (int64_t km : { (int64_t) 1, (int64_t) 3 }) {
-                for (auto nk : { std::make_pair(NQKV, H), std::make_pair(H, QD), std::make_pair(QD, H), std::make_pair(2 * F, H),
+                for (auto nk : { std::make_pair(NQKV, H), std::make_pair(H, QD), std::make_pair(2 * F, H),
                                  std::make_pair(H, F), std::make_pair(2 * KD, H), std::make_pair(H, in_ch * P),
                                  std::make_pair(Oc * P, H), std::make_pair(H, (size_t) c.enc_hidden_size),
                                  std::make_pair(6 * H, H), std::make_pair(H, H), std::make_pair(H, (size_t) 256) }) {

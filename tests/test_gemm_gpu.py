@@ -168,41 +168,3 @@ def test_gemm_cta_pairs(cuda, f16):
     d = (Cb.float() - base).abs()
     ulp = 2.0 ** -10 if f16 else 2.0 ** -8
     assert (d <= base.abs() * ulp + 2e-5 * base.abs().max()).all()
-
-
-@pytest.mark.parametrize("M,N,K,f16", [(6000, 2048, 2048, False), (6000, 2048, 6144, True), (6000, 4096, 1024, True),
-                                       (2500, 2000, 1024, False)])
-def test_gemm_tail_split(cuda, M, N, K, f16):
-    """When the last wave of output tiles is partial, its tiles are split along K over the idle SMs
-    and the last split of each tile to finish sums the splits in split order (acb_gemm_tc with a
-    workspace). Every epilogue against the fp32 reference; repeat runs bit-identical; the same
-    result bits as the unsplit GEMM are not required (fp32 summation order differs)."""
-    import torch
-    ws_bytes = acb.gemm_workspace_bytes(M, N, K)
-    assert ws_bytes > 0, "these shapes leave a partial last wave"
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
-    dt = torch.float16 if f16 else torch.bfloat16
-    g = torch.Generator(device=cuda).manual_seed(M + N + K)
-    S = 4
-    T = (M + S - 1) // S
-    A = torch.randn(M, K, device=cuda, generator=g).to(dt)
-    B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).to(dt)
-    bias = torch.randn(N, device=cuda, generator=g)
-    res = torch.randn(M, N, device=cuda, generator=g)
-    gate = torch.randn(S, N, device=cuda, generator=g)
-    base = ref_mm(A, B)
-    err = torch.zeros(1, dtype=torch.int32, device=cuda)
-    C1 = acb.gemm_bf16(A, B, workspace=ws, err=err)
-    C2 = acb.gemm_bf16(A, B, workspace=ws, err=err)
-    torch.cuda.synchronize()
-    assert int(err.item()) == 0
-    assert max_rel(C1.cpu().numpy(), base.cpu().numpy()) <= 1e-5
-    assert torch.equal(C1, C2)
-    out = res.clone()
-    acb.gemm_bf16(A, B, out=out, bias=bias, res=out, gate=gate, rows_per_sample=T, workspace=ws)
-    want = res + (base + bias) * gate.repeat_interleave(T, dim=0)[:M]
-    assert max_rel((out - res).cpu().numpy(), (want - res).cpu().numpy()) <= 1e-5
-    Ch = acb.gemm_bf16(A, B, out_dtype=dt, workspace=ws)
-    d = (Ch.float() - base).abs()
-    ulp = 2.0 ** -10 if f16 else 2.0 ** -8
-    assert (d <= base.abs() * ulp + 2e-5 * base.abs().max()).all()
