@@ -124,6 +124,7 @@ def lib():
             "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
             "acb_vec_dot_type": (I, [I]),
             "acb_gemm_workspace_bytes": (C.c_size_t, [I64, I64, I64]),
+            "acb_gemm_swiglu_quant": (I, [P, I64, P, I64, I64, I64, I64, P, I, I, P, I, I64, I, P, P]),
             "acb_gemm_pair_clusters": (I, [I]),
             "acb_gemm_tc": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, C.c_size_t, P,
                                 P]),
@@ -402,6 +403,21 @@ def gemm_bf16(A, B, out=None, out_dtype=None, bias=None, res=None, gate=None, ro
         _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, N, K, _ptr(out), dtype_id(out), out.stride(0), _ptr(bias),
         _ptr(res), res.stride(0) if res is not None else 0, _ptr(gate), gs, rows_per_sample or M, flags,
         _ptr(workspace), wsb, _ptr(err), _stream(stream)))
+    return out
+
+
+def gemm_swiglu_quant(A, B, F, vec_type, layout, bias=None, err=None, stream=None):
+    """acb_gemm_swiglu_quant: A [M, K] and B [2F, K] (gate rows then up rows) 16-bit -> the down
+    projection's operand [M, F] (PLAIN) or [M, 3F] (GEMM_A), f16 (bf16 for vec_type BF16)."""
+    import torch
+    M, K = A.shape
+    width = 3 * F if layout == LAYOUT_GEMM_A else F
+    dt = torch.bfloat16 if vec_type == BF16 else torch.float16
+    out = torch.empty((M, width), dtype=dt, device=A.device)
+    flags = FLAG_F16 if A.dtype == torch.float16 else 0
+    _check("acb_gemm_swiglu_quant", lib().acb_gemm_swiglu_quant(
+        _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, F, K, _ptr(bias), vec_type, layout, _ptr(out), dtype_id(out),
+        width, flags, _ptr(err), _stream(stream)))
     return out
 
 

@@ -62,6 +62,12 @@ struct GemmArgs {
     int64_t       gate_stride;
     int64_t       rows_per_sample;
     int *         err;
+    // SwiGLU epilogue (swiglu != 0): B is [gate rows F | up rows F]; output tile t covers features
+    // [128 nt, 128 nt + 128) (accumulator columns 0..127 gate, 128..255 up); C receives the
+    // down projection's activation operand: silu(gate) * up quantised as vec type sw_vt, layout
+    // sw_layout (PLAIN [M][F] or GEMM_A [M][3F]), 16-bit, ldc elements per row
+    int           swiglu, sw_vt, sw_layout;
+    int64_t       F;
     int           splits;  // split-K factor; > 1: raw partials to ws, epilogue by splitk_reduce_kernel
     int           kps;     // k-tiles per split
     float *       ws;      // [splits][M][N] f32 partial accumulators
@@ -108,6 +114,101 @@ __device__ __forceinline__ float4 load_cols(const float * src, int ncol) {
                        ncol > 3 ? src[3] : 0.0f);
 }
 
+// SwiGLU epilogue of one warp: its 32 rows (m_base + lane) of the tile, features f0 .. f0+127.
+// Per 32-feature group: silu(gate) * up (ggml_swiglu, the unfused acb_act_quant_swiglu
+// arithmetic), then one Q8_0 block per row (d = amax / 127 stored as f16, q = round(y / d)) or a
+// plain 16-bit rounding, then the 16-bit operand planes (GEMM_A: hi at f, hi at F + f, lo at 2F +
+// f; PLAIN: hi at f), staged through shared memory so each row segment is written whole.
+__device__ __forceinline__ void swiglu_epilogue(const GemmArgs & g, uint32_t tacc, int64_t m_base, int64_t f0,
+                                                int lane, float * stg) {
+    const int64_t m  = m_base + lane;
+    const bool    bf = g.sw_vt == ACB_TYPE_BF16;
+    uint32_t *    sw = reinterpret_cast<uint32_t *>(stg);  // [32 rows][20 words]: 16 words of row data
+#pragma unroll 1
+    for (int c = 0; c < 4; c++) {
+        uint32_t rg[32], ru[32];
+        tmem_ld32(tacc + (uint32_t) (c * 32), rg);
+        tmem_ld32(tacc + (uint32_t) (128 + c * 32), ru);
+        if (m_base >= g.M) {
+            continue;  // warp-uniform
+        }
+        const int64_t f = f0 + c * 32;
+        float         y[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            float gv = __uint_as_float(rg[j]), uv = __uint_as_float(ru[j]);
+            if (g.bias) {
+                gv = __fadd_rn(gv, g.bias[f + j]);
+                uv = __fadd_rn(uv, g.bias[g.F + f + j]);
+            }
+            y[j] = silu_times(gv, uv);
+        }
+        if (g.sw_vt == ACB_TYPE_Q8_0) {
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                amax = fmaxf(amax, fabsf(y[j]));
+            }
+            const float d  = __fdiv_rn(amax, 127.0f);
+            const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+            const float dh = __half2float(__float2half_rn(d));  // the block stores d as f16
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                y[j] = __fmul_rn(dh, (float) (int) roundf(__fmul_rn(y[j], id)));
+            }
+        }
+        const int nplanes = g.sw_layout == ACB_LAYOUT_GEMM_A ? 2 : 1;
+        for (int pl = 0; pl < nplanes; pl++) {
+            // this row's 32 values of the plane as 16 packed words
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint32_t wv[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float a = y[j + 2 * e], b = y[j + 2 * e + 1];
+                    if (bf) {
+                        __nv_bfloat162 hb = __floats2bfloat162_rn(a, b);
+                        if (pl == 1) {
+                            const float2 hf2 = __bfloat1622float2(hb);
+                            hb               = __floats2bfloat162_rn(__fsub_rn(a, hf2.x), __fsub_rn(b, hf2.y));
+                        }
+                        wv[e] = *reinterpret_cast<uint32_t *>(&hb);
+                    } else {
+                        __half2 hh = __floats2half2_rn(a, b);
+                        if (pl == 1) {
+                            const float2 hf2 = __half22float2(hh);
+                            hh               = __floats2half2_rn(__fsub_rn(a, hf2.x), __fsub_rn(b, hf2.y));
+                        }
+                        wv[e] = *reinterpret_cast<uint32_t *>(&hh);
+                    }
+                }
+                *reinterpret_cast<uint4 *>(sw + lane * 20 + j / 2) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+            __syncwarp();
+            // 8 rows per pass, 4 lanes x 16 bytes per row
+#pragma unroll
+            for (int it = 0; it < 4; it++) {
+                const int     rr = it * 8 + (lane >> 2), part = lane & 3;
+                const int64_t mr = m_base + rr;
+                if (mr < g.M) {
+                    const uint4 v   = *reinterpret_cast<const uint4 *>(sw + rr * 20 + part * 4);
+                    uint16_t *  dst = reinterpret_cast<uint16_t *>(g.C) + mr * g.ldc + f + part * 8;
+                    if (pl == 0) {
+                        *reinterpret_cast<uint4 *>(dst) = v;
+                        if (g.sw_layout == ACB_LAYOUT_GEMM_A) {
+                            *reinterpret_cast<uint4 *>(dst + g.F) = v;
+                        }
+                    } else {
+                        *reinterpret_cast<uint4 *>(dst + 2 * g.F) = v;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+    (void) m;
+}
+
 // ---- the kernel ------------------------------------------------------------------------------------
 template <bool F16, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -130,7 +231,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool     leader = rank == 0;
     const int64_t  unit    = PAIR ? (blockIdx.x >> 1) : blockIdx.x;  // work-issuing unit: CTA or CTA pair
     const int64_t  n_units = PAIR ? (gridDim.x >> 1) : gridDim.x;
-    const int64_t m_tiles = (g.M + Cf::kTileM - 1) / Cf::kTileM, n_tiles = (g.N + kBN - 1) / kBN;
+    const int64_t m_tiles = (g.M + Cf::kTileM - 1) / Cf::kTileM;
+    const int64_t n_tiles = g.swiglu ? g.F / 128 : (g.N + kBN - 1) / kBN;
     const int64_t tiles   = m_tiles * n_tiles;
     const int64_t n_work  = tiles * g.splits;
     const int     k_tiles = (int) (g.K / kBK);
@@ -179,7 +281,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const int64_t t  = w % tiles;
                 const int     sp = (int) (w / tiles);
                 const int ma = (int) ((t % m_tiles) * Cf::kTileM) + (int) rank * 128;  // this CTA's A rows
-                const int nb = (int) ((t / m_tiles) * kBN) + (int) rank * Cf::kRowsB;  // this CTA's B rows
+                // this CTA's B rows (SwiGLU: 128 gate rows and the matching 128 up rows per tile)
+                const int nb = g.swiglu ? (int) ((t / m_tiles) * 128) + (int) rank * (int) g.F
+                                        : (int) ((t / m_tiles) * kBN) + (int) rank * Cf::kRowsB;
                 const int kt1 = min(k_tiles, (sp + 1) * g.kps);
                 for (int kt = sp * g.kps; kt < kt1; kt++, it++) {
                     const int s = it % Cf::kStages;
@@ -199,7 +303,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     } else {
                         ptx::mbar_arrive_expect_tx(&full[s], Cf::kTx);
                         tma_load_2d(st, &tmA, kt * kBK, ma, &full[s]);
-                        tma_load_2d(st + Cf::kATile, &tmB, kt * kBK, nb, &full[s]);
+                        if (g.swiglu) {  // two 128-row boxes: gate rows, then up rows
+                            tma_load_2d(st + Cf::kATile, &tmB, kt * kBK, nb, &full[s]);
+                            tma_load_2d(st + Cf::kATile + 128 * kBK * 2, &tmB, kt * kBK, nb + (int) g.F, &full[s]);
+                        } else {
+                            tma_load_2d(st + Cf::kATile, &tmB, kt * kBK, nb, &full[s]);
+                        }
                     }
                 }
             }
@@ -276,6 +385,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_after();
             const int64_t t      = w % tiles;
             const int64_t m_base = (t % m_tiles) * Cf::kTileM + (int64_t) rank * 128 + q * 32;
+            if (g.swiglu) {
+                swiglu_epilogue(g, tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN), m_base,
+                                (t / m_tiles) * 128, lane, stg);
+            } else {
             const int64_t n0     = (t / m_tiles) * kBN;
             const bool    part   = g.splits > 1;  // raw partial of split w / tiles
             float *       pws    = part ? g.ws + (w / tiles) * g.M * g.N : nullptr;
@@ -339,6 +452,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 __syncwarp();
             }
+            }  // plain / split epilogue
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -598,6 +712,90 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
         cfg.attrs           = &pdl;
         cfg.numAttrs        = 1;
         e                   = cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, g);
+    }
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_gemm_swiglu_quant(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M,
+                                            int64_t F, int64_t K, const float * bias, int vec_type, int layout,
+                                            void * Y, int y_type, int64_t ldy, int flags, int * err_flag,
+                                            acb_stream_t stream) {
+    if (!A || !B || !Y || M <= 0 || F <= 0 || K <= 0 || lda < K || ldb < K) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (F % 128 != 0 || K % kBK != 0 || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(A) % 16 != 0 || reinterpret_cast<uintptr_t>(B) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(Y) % 16 != 0 || ldy % 8 != 0) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if ((vec_type != ACB_TYPE_Q8_0 && vec_type != ACB_TYPE_F16 && vec_type != ACB_TYPE_BF16) ||
+        (layout != ACB_LAYOUT_PLAIN && layout != ACB_LAYOUT_GEMM_A) ||
+        y_type != (vec_type == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (ldy < (layout == ACB_LAYOUT_GEMM_A ? 3 * F : F)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    GemmArgs g        = {};
+    g.M               = M;
+    g.N               = 2 * F;
+    g.K               = K;
+    g.C               = Y;
+    g.c_type          = y_type;
+    g.ldc             = ldy;
+    g.bias            = bias;
+    g.rows_per_sample = 1;
+    g.err             = err_flag;
+    g.splits          = 1;
+    g.kps             = (int) (K / kBK);
+    g.swiglu          = 1;
+    g.sw_vt           = vec_type;
+    g.sw_layout       = layout;
+    g.F               = F;
+    const bool f16      = (flags & ACB_FLAG_F16) != 0;
+    const int  clusters = M > 128 ? pair_clusters(f16) : 0;
+    const bool pair     = clusters > 0;
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, 2 * F, K, ldb, 128, f16)) {
+        return ACB_ERR_CUDA;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim           = dim3(kGemmThreads);
+    cfg.stream             = (cudaStream_t) stream;
+    cudaLaunchAttribute attr[2];
+    int                 na = 0;
+    if (pair) {
+        attr[na].id               = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 2;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    if (flags & ACB_FLAG_PDL) {
+        attr[na].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    cfg.attrs    = na ? attr : nullptr;
+    cfg.numAttrs = na;
+    cudaError_t e;
+    if (pair) {
+        const int64_t work = ((M + 255) / 256) * (F / 128);
+        cfg.gridDim          = dim3((unsigned) (2 * (work < clusters ? work : clusters)));
+        cfg.dynamicSmemBytes = GemmCfg<true>::kSmem;
+        e = cudaLaunchKernelEx(&cfg, f16 ? gemm_tc_kernel<true, true> : gemm_tc_kernel<false, true>, ta, tb, g);
+    } else {
+        const int64_t work = ((M + 127) / 128) * (F / 128);
+        void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
+            f16 ? gemm_tc_kernel<true, false> : gemm_tc_kernel<false, false>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) GemmCfg<false>::kSmem);
+        cfg.gridDim          = dim3((unsigned) (work < num_sms() ? work : num_sms()));
+        cfg.dynamicSmemBytes = GemmCfg<false>::kSmem;
+        e                    = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
     }
     if (e != cudaSuccess) {
         set_last_cuda_error(e);

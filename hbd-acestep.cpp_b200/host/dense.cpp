@@ -81,4 +81,40 @@ acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int
                        rows_per_sample, ACB_FLAG_PDL | L.op, s.ws, s.ws_bytes, s.err, (acb_stream_t) st);
 }
 
+acb_status dense_ffn(const DenseLinear & Lgu, const DenseLinear & Ldown, bool exact, const float * x, int64_t xs,
+                     int M, float * out, int64_t ldo, const float * res, int64_t ldr, const float * gate,
+                     int64_t gate_stride, int64_t rows_per_sample, void * gu_buf, const DenseScratch & s,
+                     cudaStream_t st, const NormSpec * norm) {
+    const int64_t F         = Ldown.K;
+    const bool    down3     = exact && Ldown.split;
+    const int     vt        = Ldown.vec;
+    const bool    fusable   = Lgu.N == 2 * F && F % 128 == 0 && M >= kFfnFuseMinRows &&
+                         (vt == ACB_TYPE_Q8_0 || vt == ACB_TYPE_F16 || vt == ACB_TYPE_BF16) &&
+                         Lgu.op == Ldown.op;
+    if (!fusable) {
+        ACB_TRY(dense_forward(Lgu, exact, x, xs, 0, M, gu_buf, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0,
+                              s, st, norm));
+        return dense_forward(Ldown, exact, static_cast<const float *>(gu_buf), 2 * F, F, M, out, ACB_TYPE_F32, ldo,
+                             nullptr, res, ldr, gate, gate_stride, rows_per_sample, s, st);
+    }
+    // activation of the gate/up projection
+    const bool    three  = exact && Lgu.split;
+    const int64_t Kp     = three ? 3 * (int64_t) Lgu.K : Lgu.K;
+    const int     layout = three ? ACB_LAYOUT_GEMM_A : ACB_LAYOUT_PLAIN;
+    if (norm) {
+        ACB_TRY(acb_norm_quant(x, xs, M, Lgu.K, norm->w, norm->eps, norm->scale, norm->shift, norm->vec_stride,
+                               norm->rows_per_sample, Lgu.vec, layout, s.xq, Lgu.act_type(), Kp, 0, (acb_stream_t) st));
+    } else {
+        ACB_TRY(acb_act_quant_ex(x, xs, 0, M, Lgu.K, Lgu.vec, layout, s.xq, Lgu.act_type(), Kp, 0, (acb_stream_t) st));
+    }
+    // gate/up GEMM with SwiGLU and the down projection's quantisation in its epilogue
+    const int64_t Kd = down3 ? 3 * F : F;
+    ACB_TRY(acb_gemm_swiglu_quant(s.xq, Kp, Lgu.w, Lgu.ldw, M, F, Kp, nullptr, vt,
+                                  down3 ? ACB_LAYOUT_GEMM_A : ACB_LAYOUT_PLAIN, gu_buf, Ldown.act_type(), Kd,
+                                  ACB_FLAG_PDL | Lgu.op, s.err, (acb_stream_t) st));
+    return acb_gemm_tc(gu_buf, Kd, Ldown.w, Ldown.ldw, M, Ldown.N, Kd, out, ACB_TYPE_F32, ldo, nullptr, res, ldr, gate,
+                       gate_stride, rows_per_sample, ACB_FLAG_PDL | Ldown.op, s.ws, s.ws_bytes, s.err,
+                       (acb_stream_t) st);
+}
+
 }  // namespace acb

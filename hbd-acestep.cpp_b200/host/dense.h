@@ -70,4 +70,18 @@ acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int
                          const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
                          cudaStream_t st, const NormSpec * norm = nullptr);
 
+// Rows from which the feed-forward block runs its gate/up GEMM with the SwiGLU epilogue (the
+// fused form needs whole waves of 256-row tiles to pay off; fewer rows take the split-K path).
+constexpr int kFfnFuseMinRows = 1024;
+
+// Feed-forward block out = epi(down(swiglu(gate_up(x)))) (ggml_swiglu between the two
+// projections, src/dit-graph.h:259-268, src/qwen3-enc.h:217-223): x f32 [M][xs] (normalised
+// first by `norm` when given), out f32 [M][ldo] with res / gate as acb_gemm_tc. gu_buf holds
+// max(M * 2F f32, M * 3F 16-bit) bytes: the f32 gate/up product, or, when the gate/up GEMM
+// fuses SwiGLU and the down projection's quantisation into its epilogue, that operand.
+acb_status dense_ffn(const DenseLinear & Lgu, const DenseLinear & Ldown, bool exact, const float * x, int64_t xs,
+                     int M, float * out, int64_t ldo, const float * res, int64_t ldr, const float * gate,
+                     int64_t gate_stride, int64_t rows_per_sample, void * gu_buf, const DenseScratch & s,
+                     cudaStream_t st, const NormSpec * norm = nullptr);
+
 }  // namespace acb

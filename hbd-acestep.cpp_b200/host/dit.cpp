@@ -253,7 +253,7 @@ acb_status acb_dit::condition(cudaStream_t s) {
 acb_status acb_dit::layer(int l, cudaStream_t s) {
     const DiTLayerW &  L = layers[(size_t) l];
     const int          H = c.hidden_size, D = c.head_dim, Nh = c.n_heads, Nkv = c.n_kv_heads;
-    const int          QD = qd(), KD = kvd(), NQKV = nqkv(), F = c.intermediate_size;
+    const int          QD = qd(), KD = kvd(), NQKV = nqkv();
     const int          R = Ng * S;
     const float        eps   = c.rms_norm_eps;
     const float        scale = 1.0f / sqrtf((float) D);
@@ -338,10 +338,7 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ns_ff.w        = (const float *) L.mlp_norm->data;
     ns_ff.scale    = scale_ff;
     ns_ff.shift    = shift_ff;
-    ACB_TRY(dense_forward(L.gu, exact, hp, H, 0, R, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0, sc,
-                          s, &ns_ff));
-    return dense_forward(L.down, exact, gu.as<float>(), 2 * F, F, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_ff, 0, R,
-                         sc, s);
+    return dense_ffn(L.gu, L.down, exact, hp, H, R, hp, H, hp, H, gate_ff, 0, R, gu.p, sc, s, &ns_ff);
 }
 
 // ---- one evaluation: input [Ng][T][in_ch] in `input` -> velocity in `vel` ---------------------------

@@ -148,7 +148,7 @@ acb_status acb_qwen3_enc::reserve(int S) {
 
 // Layers [l0, l1) over the hidden states in `h` (qwen3_build_layers, qwen3-enc.h:249-262).
 acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) {
-    const int          H = c.hidden_size, F = c.intermediate_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
+    const int          H = c.hidden_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
     const int          QD = Nh * D, KD = Nkv * D, NQKV = nqkv();
     const float        eps   = c.rms_norm_eps;
     const float        scale = 1.0f / sqrtf((float) D);
@@ -200,10 +200,7 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
         NormSpec ns_post;
         ns_post.w   = (const float *) L.post_norm->data;
         ns_post.eps = eps;
-        ACB_TRY(dense_forward(L.gu, exact, hp, H, 0, S, gu.p, ACB_TYPE_F32, 2 * F, nullptr, nullptr, 0, nullptr, 0, 0,
-                              sc, s, &ns_post));
-        ACB_TRY(dense_forward(L.down, exact, gu.as<float>(), 2 * F, F, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr,
-                              0, 0, sc, s));
+        ACB_TRY(dense_ffn(L.gu, L.down, exact, hp, H, S, hp, H, hp, H, nullptr, 0, 0, gu.p, sc, s, &ns_post));
     }
     return ACB_OK;
 }

@@ -234,6 +234,19 @@ ACB_API acb_status acb_gemm_bf16(const void * A, int64_t lda, const void * B, in
  * in split order (deterministic) and applies the epilogue. acb_gemm_workspace_bytes gives the
  * bytes needed at these sizes (0: no split is used); a smaller or NULL workspace runs unsplit.
  * Calls sharing one workspace must not overlap. */
+/* The gate/up projection of a feed-forward block with SwiGLU and the down projection's activation
+ * quantisation fused into its epilogue: Y = from_float(silu(A.Bg^T [+ bg]) * (A.Bu^T [+ bu])),
+ * B = [Bg (F rows) | Bu (F rows)] stacked [2F][ldb] (bias, if given, [2F] in the same order),
+ * quantised as acb_act_quant_ex does for vec_type Q8_0, F16 or BF16 (layout PLAIN [M][F] or
+ * GEMM_A [M][3F] hi|hi|lo), y_type F16 (BF16 for vec_type BF16), ldy elements per row. Replaces
+ * the two ggml_mul_mat, ggml_swiglu and the down mul_mat's from_float of dit_ggml_build_layer
+ * (src/dit-graph.h:259-268) and the encoder FFN (src/qwen3-enc.h:217-223); bit-identical to
+ * acb_gemm_tc (f32 out) + acb_act_quant_ex(..., up_offset = F, ...). F a multiple of 128. */
+ACB_API acb_status acb_gemm_swiglu_quant(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M,
+                                         int64_t F, int64_t K, const float * bias, int vec_type, int layout,
+                                         void * Y, int y_type, int64_t ldy, int flags, int * err_flag,
+                                         acb_stream_t stream);
+
 ACB_API size_t     acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 /* Unsplit GEMMs with M > 128 run on CTA pairs (clusters of two, tcgen05 cta_group::2, 256 x 256

@@ -168,3 +168,27 @@ def test_gemm_cta_pairs(cuda, f16):
     d = (Cb.float() - base).abs()
     ulp = 2.0 ** -10 if f16 else 2.0 ** -8
     assert (d <= base.abs() * ulp + 2e-5 * base.abs().max()).all()
+
+
+@pytest.mark.parametrize("M,F,K,f16,vt,layout,bias", [
+    (2500, 1024, 1024, True, O.Q8_0, acb.LAYOUT_GEMM_A, False),
+    (6000, 3072, 2048, True, O.Q8_0, acb.LAYOUT_PLAIN, False),
+    (300, 1024, 512, False, O.Q8_0, acb.LAYOUT_GEMM_A, True),
+    (1000, 1024, 1024, True, O.F16, acb.LAYOUT_PLAIN, True),
+    (1000, 1024, 1024, False, O.BF16, acb.LAYOUT_PLAIN, False)])
+def test_gemm_swiglu_quant_matches_unfused(cuda, M, F, K, f16, vt, layout, bias):
+    """acb_gemm_swiglu_quant (SwiGLU and the down projection's quantisation in the gate/up GEMM's
+    epilogue) == acb_gemm_tc (f32 out, same bias) + acb_act_quant_ex(up_offset = F), bit for bit."""
+    import torch
+    dt = torch.float16 if f16 else torch.bfloat16
+    g = torch.Generator(device=cuda).manual_seed(M + F + K)
+    A = torch.randn(M, K, device=cuda, generator=g).to(dt)
+    B = (torch.randn(2 * F, K, device=cuda, generator=g) * 0.05).to(dt)
+    bv = torch.randn(2 * F, device=cuda, generator=g) if bias else None
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    got = acb.gemm_swiglu_quant(A, B, F, vt, layout, bias=bv, err=err)
+    gu = acb.gemm_bf16(A, B, bias=bv)
+    want = acb.act_quant_ex(gu, F, vt, layout, up_offset=F)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
