@@ -68,6 +68,7 @@ struct GemmArgs {
     // sw_layout (PLAIN [M][F] or GEMM_A [M][3F]), 16-bit, ldc elements per row
     int           swiglu, sw_vt, sw_layout;
     int64_t       F;
+    int           group_m;  // tile order: groups of group_m m-tiles, n-tiles outer within a group, m inner
     int           splits;  // split-K factor; > 1: raw partials to ws, epilogue by splitk_reduce_kernel
     int           kps;     // k-tiles per split
     float *       ws;      // [splits][M][N] f32 partial accumulators
@@ -209,6 +210,18 @@ __device__ __forceinline__ void swiglu_epilogue(const GemmArgs & g, uint32_t tac
     (void) m;
 }
 
+// (m-tile, n-tile) of tile t: tiles run in groups of group_m m-tiles; within a group the m-tile
+// varies fastest, so a wave of resident CTAs touches a compact block of A rows and B rows
+__device__ __forceinline__ void tile_mn(int64_t t, int64_t m_tiles, int64_t n_tiles, int group_m, int64_t & mt,
+                                        int64_t & nt) {
+    const int64_t gsz = (int64_t) group_m * n_tiles;
+    const int64_t grp = t / gsz, idx = t - grp * gsz;
+    const int64_t m0  = grp * group_m;
+    const int64_t gm  = m_tiles - m0 < group_m ? m_tiles - m0 : group_m;
+    mt                = m0 + idx % gm;
+    nt                = idx / gm;
+}
+
 // ---- the kernel ------------------------------------------------------------------------------------
 template <bool F16, bool PAIR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -280,10 +293,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int64_t w = unit; w < n_work && !abort_flag; w += n_units) {
                 const int64_t t  = w % tiles;
                 const int     sp = (int) (w / tiles);
-                const int ma = (int) ((t % m_tiles) * Cf::kTileM) + (int) rank * 128;  // this CTA's A rows
+                int64_t mt, nt;
+                tile_mn(t, m_tiles, n_tiles, g.group_m, mt, nt);
+                const int ma = (int) (mt * Cf::kTileM) + (int) rank * 128;  // this CTA's A rows
                 // this CTA's B rows (SwiGLU: 128 gate rows and the matching 128 up rows per tile)
-                const int nb = g.swiglu ? (int) ((t / m_tiles) * 128) + (int) rank * (int) g.F
-                                        : (int) ((t / m_tiles) * kBN) + (int) rank * Cf::kRowsB;
+                const int nb = g.swiglu ? (int) (nt * 128) + (int) rank * (int) g.F
+                                        : (int) (nt * kBN) + (int) rank * Cf::kRowsB;
                 const int kt1 = min(k_tiles, (sp + 1) * g.kps);
                 for (int kt = sp * g.kps; kt < kt1; kt++, it++) {
                     const int s = it % Cf::kStages;
@@ -384,12 +399,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_after();
             const int64_t t      = w % tiles;
-            const int64_t m_base = (t % m_tiles) * Cf::kTileM + (int64_t) rank * 128 + q * 32;
+            int64_t mt, nt;
+            tile_mn(t, m_tiles, n_tiles, g.group_m, mt, nt);
+            const int64_t m_base = mt * Cf::kTileM + (int64_t) rank * 128 + q * 32;
             if (g.swiglu) {
                 swiglu_epilogue(g, tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN), m_base,
-                                (t / m_tiles) * 128, lane, stg);
+                                nt * 128, lane, stg);
             } else {
-            const int64_t n0     = (t / m_tiles) * kBN;
+            const int64_t n0     = nt * kBN;
             const bool    part   = g.splits > 1;  // raw partial of split w / tiles
             float *       pws    = part ? g.ws + (w / tiles) * g.M * g.N : nullptr;
 #pragma unroll 1
@@ -561,6 +578,17 @@ static bool make_map(CUtensorMap * m, const void * base, int64_t rows, int64_t K
 
 // Clusters of two CTAs that can be resident at once for the pair kernel (0: pairs off). Cached
 // per operand type; ACB_GEMM_PAIR=0 in the environment turns the pair kernel off.
+// Tile-order group (m-tiles per group); ACB_GEMM_GROUP in the environment overrides it.
+static int group_m_for(int64_t m_tiles) {
+    static int env = -1;
+    if (env < 0) {
+        const char * e = getenv("ACB_GEMM_GROUP");
+        env            = e ? atoi(e) : 0;
+    }
+    const int gm = env > 0 ? env : (int) m_tiles;
+    return gm < 1 ? 1 : (gm > m_tiles ? (int) m_tiles : gm);
+}
+
 static int pair_clusters(bool f16) {
     static int n[2] = { -1, -1 };
     int &      c    = n[f16 ? 1 : 0];
@@ -668,6 +696,7 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
     if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, N, K, ldb, pair ? 128 : kBN, f16)) {
         return ACB_ERR_CUDA;
     }
+    g.group_m              = group_m_for(pair ? (M + 255) / 256 : (M + 127) / 128);
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim           = dim3(kGemmThreads);
     cfg.stream             = (cudaStream_t) stream;
@@ -763,6 +792,7 @@ extern "C" acb_status acb_gemm_swiglu_quant(const void * A, int64_t lda, const v
     if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, 2 * F, K, ldb, 128, f16)) {
         return ACB_ERR_CUDA;
     }
+    g.group_m              = group_m_for(pair ? (M + 255) / 256 : (M + 127) / 128);
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim           = dim3(kGemmThreads);
     cfg.stream             = (cudaStream_t) stream;
