@@ -254,6 +254,7 @@ PRO_X, PRO_RMSNORM, PRO_SUM_SPLITS, PRO_SWIGLU = 0, 1, 2, 3
 EPI_STORE, EPI_ADD = 0, 1
 FLAG_PDL = 1
 FLAG_F16 = 2  # tensor-core operands are f16 (acb_gemm_bf16, acb_attn_prefill)
+FLAG_GEMM_A = 4  # acb_attn_tc: quantised output in the exact [hi | hi | lo] operand layout
 
 
 def gemv(W, w_type, N, K, x, M=None, prologue=PRO_X, x_stride=None, norm_w=None, eps=1e-6, n_split=1, y=None,
@@ -735,15 +736,28 @@ def attn_vt(v, Nkv, lo=False, vt_ld=None, out=None, stream=None):
 
 
 def attn_tc(q, k, vt, vt_ld, Nh, Nkv, Sq, Skv, batch, mask=MASK_NONE, window=0, causal_off=0, out=None,
-            out_dtype=None, scale=None, q_lo=0, k_lo=0, vt_lo=0, flags=0, err=None, stream=None):
-    """q [batch*Sq, q_ts], k [batch*Skv, k_ts] f16 (views allowed), vt from attn_vt -> o [batch*Sq, Nh*128]."""
+            out_dtype=None, scale=None, q_lo=0, k_lo=0, vt_lo=0, flags=0, err=None, stream=None, quant=None,
+            gemm_a=False):
+    """q [batch*Sq, q_ts], k [batch*Skv, k_ts] f16 (views allowed), vt from attn_vt -> o [batch*Sq, Nh*128].
+    quant=Q8_0 (or F16 / BF16): the output projection's operand instead (16-bit; with gemm_a the
+    [hi | hi | lo] layout, 3*Nh*128 columns)."""
     import math
 
     import torch
+    o_type = None
+    if quant is not None:
+        o_type = quant
+        width = (3 if gemm_a else 1) * Nh * 128
+        if out is None:
+            out = torch.empty((batch * Sq, width), dtype=torch.bfloat16 if quant == BF16 else torch.float16,
+                              device=q.device)
+        if gemm_a:
+            flags |= FLAG_GEMM_A
     if out is None:
         out = torch.empty((batch * Sq, Nh * 128), dtype=out_dtype or torch.float32, device=q.device)
     _check("acb_attn_tc", lib().acb_attn_tc(
-        _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(vt), vt_ld, _ptr(out), dtype_id(out), out.stride(0), batch,
+        _ptr(q), q.stride(0), _ptr(k), k.stride(0), _ptr(vt), vt_ld, _ptr(out),
+        o_type if o_type is not None else dtype_id(out), out.stride(0), batch,
         Sq, Skv, Nh, Nkv, 128, mask, window, causal_off, scale if scale is not None else 1.0 / math.sqrt(128), flags,
         q_lo, k_lo, vt_lo, _ptr(err), _stream(stream)))
     return out

@@ -52,6 +52,8 @@ struct AttnTcArgs {
     int     window, causal_off;
     float   scale_log2;
     int *   err;
+    int     gemm_a;  // 16-bit output as [hi | hi | lo] planes Nh*128 columns apart
+    int64_t o_k;     // Nh*128
 };
 
 template <bool SPLIT> struct TcLayout {
@@ -487,22 +489,60 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                            __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
                     }
                 } else {
-                    uint32_t pk[16];
+                    // 16-bit output; Q8_0: these 32 columns are one block of the output projection's
+                    // quantised operand (ggml from_float: d = amax / 127 stored as f16, q = round(y / d))
+                    float y[32];
 #pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const float v0 = __uint_as_float(o[2 * e]) * inv, v1 = __uint_as_float(o[2 * e + 1]) * inv;
-                        if (a.o_type == ACB_TYPE_F16) {
-                            __half2 hh = __floats2half2_rn(v0, v1);
-                            pk[e]      = *reinterpret_cast<uint32_t *>(&hh);
-                        } else {
-                            __nv_bfloat162 bb = __floats2bfloat162_rn(v0, v1);
-                            pk[e]             = *reinterpret_cast<uint32_t *>(&bb);
+                    for (int e = 0; e < 32; e++) {
+                        y[e] = __uint_as_float(o[e]) * inv;
+                    }
+                    if (a.o_type == ACB_TYPE_Q8_0) {
+                        float amax = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            amax = fmaxf(amax, fabsf(y[e]));
+                        }
+                        const float d  = __fdiv_rn(amax, 127.0f);
+                        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                        const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+                        for (int e = 0; e < 32; e++) {
+                            y[e] = __fmul_rn(dh, (float) (int) roundf(__fmul_rn(y[e], id)));
                         }
                     }
-                    uint4 * d = reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(a.o) + base);
+                    const bool bfo = a.o_type == ACB_TYPE_BF16;
+                    uint32_t   pk[16], pl[16];
+#pragma unroll
+                    for (int e = 0; e < 16; e++) {
+                        const float v0 = y[2 * e], v1 = y[2 * e + 1];
+                        if (bfo) {
+                            __nv_bfloat162 bb = __floats2bfloat162_rn(v0, v1);
+                            pk[e]             = *reinterpret_cast<uint32_t *>(&bb);
+                            const float2 f2   = __bfloat1622float2(bb);
+                            __nv_bfloat162 ll = __floats2bfloat162_rn(__fsub_rn(v0, f2.x), __fsub_rn(v1, f2.y));
+                            pl[e]             = *reinterpret_cast<uint32_t *>(&ll);
+                        } else {
+                            __half2 hh      = __floats2half2_rn(v0, v1);
+                            pk[e]           = *reinterpret_cast<uint32_t *>(&hh);
+                            const float2 f2 = __half22float2(hh);
+                            __half2 ll      = __floats2half2_rn(__fsub_rn(v0, f2.x), __fsub_rn(v1, f2.y));
+                            pl[e]           = *reinterpret_cast<uint32_t *>(&ll);
+                        }
+                    }
+                    uint16_t * ob = reinterpret_cast<uint16_t *>(a.o) + base;
+                    uint4 *    d  = reinterpret_cast<uint4 *>(ob);
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         d[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+                    }
+                    if (a.gemm_a) {
+                        uint4 * d1 = reinterpret_cast<uint4 *>(ob + a.o_k);
+                        uint4 * d2 = reinterpret_cast<uint4 *>(ob + 2 * a.o_k);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            d1[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+                            d2[e] = make_uint4(pl[4 * e], pl[4 * e + 1], pl[4 * e + 2], pl[4 * e + 3]);
+                        }
                     }
                 }
             }
@@ -582,8 +622,12 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
         return ACB_ERR_INVALID_ARG;
     }
     if (head_dim != kTcD || mask < 0 || mask > 2 ||
-        (o_type != ACB_TYPE_F32 && o_type != ACB_TYPE_BF16 && o_type != ACB_TYPE_F16)) {
+        (o_type != ACB_TYPE_F32 && o_type != ACB_TYPE_BF16 && o_type != ACB_TYPE_F16 && o_type != ACB_TYPE_Q8_0)) {
         return ACB_ERR_UNSUPPORTED;
+    }
+    const bool gemm_a = (flags & ACB_FLAG_GEMM_A) != 0;
+    if (gemm_a && (o_type == ACB_TYPE_F32 || o_ts < 3 * (int64_t) Nh * kTcD)) {
+        return ACB_ERR_INVALID_ARG;
     }
     const bool split = q_lo != 0 || k_lo != 0 || vt_lo != 0;
     if (split && (q_lo == 0 || k_lo == 0 || vt_lo == 0)) {
@@ -627,6 +671,8 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     a.causal_off = causal_off;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.err        = err_flag;
+    a.gemm_a     = gemm_a ? 1 : 0;
+    a.o_k        = (int64_t) Nh * kTcD;
     const size_t smem = (size_t) (split ? TcLayout<true>::TOTAL : TcLayout<false>::TOTAL) + 1024 + 256;
     void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const AttnTcArgs) =
         nullptr;

@@ -81,6 +81,26 @@ acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int
                        rows_per_sample, ACB_FLAG_PDL | L.op, s.ws, s.ws_bytes, s.err, (acb_stream_t) st);
 }
 
+bool dense_operand_spec(const DenseLinear & L, bool exact, int * o_type, int * flags, int64_t * width) {
+    if (L.vec != ACB_TYPE_Q8_0 && L.vec != ACB_TYPE_F16 && L.vec != ACB_TYPE_BF16 && L.vec != ACB_TYPE_F32) {
+        return false;
+    }
+    const bool three = exact && L.split;
+    *o_type          = L.vec == ACB_TYPE_Q8_0 ? ACB_TYPE_Q8_0 : (L.vec == ACB_TYPE_BF16 ? ACB_TYPE_BF16 : ACB_TYPE_F16);
+    *flags           = three ? ACB_FLAG_GEMM_A : 0;
+    *width           = three ? 3 * (int64_t) L.K : L.K;
+    return true;
+}
+
+acb_status dense_forward_operand(const DenseLinear & L, bool exact, int M, void * C, int c_type, int64_t ldc,
+                                 const float * bias, const float * res, int64_t ldr, const float * gate,
+                                 int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
+                                 cudaStream_t st) {
+    const int64_t Kp = (exact && L.split) ? 3 * (int64_t) L.K : L.K;
+    return acb_gemm_tc(s.xq, Kp, L.w, L.ldw, M, L.N, Kp, C, c_type, ldc, bias, res, ldr, gate, gate_stride,
+                       rows_per_sample, ACB_FLAG_PDL | L.op, s.ws, s.ws_bytes, s.err, (acb_stream_t) st);
+}
+
 acb_status dense_ffn(const DenseLinear & Lgu, const DenseLinear & Ldown, bool exact, const float * x, int64_t xs,
                      int M, float * out, int64_t ldo, const float * res, int64_t ldr, const float * gate,
                      int64_t gate_stride, int64_t rows_per_sample, void * gu_buf, const DenseScratch & s,

@@ -70,6 +70,17 @@ acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int
                          const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
                          cudaStream_t st, const NormSpec * norm = nullptr);
 
+// How a fused producer (the attention epilogue, acb_attn_tc) writes L's activation operand into
+// s.xq itself: its o_type, flags (ACB_FLAG_GEMM_A for the exact layout) and row width. False when
+// only acb_act_quant_ex can produce it (Q8_K blocks span 256 columns).
+bool dense_operand_spec(const DenseLinear & L, bool exact, int * o_type, int * flags, int64_t * width);
+
+// C = epi(xq . W^T) for an activation operand that a fused producer already wrote to s.xq.
+acb_status dense_forward_operand(const DenseLinear & L, bool exact, int M, void * C, int c_type, int64_t ldc,
+                                 const float * bias, const float * res, int64_t ldr, const float * gate,
+                                 int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
+                                 cudaStream_t st);
+
 // Rows from which the feed-forward block runs its gate/up GEMM with the SwiGLU epilogue (the
 // fused form needs whole waves of 256-row tiles to pay off; fewer rows take the split-K path).
 constexpr int kFfnFuseMinRows = 1024;

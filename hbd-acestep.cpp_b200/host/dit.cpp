@@ -268,6 +268,19 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     const bool swa  = (l % 2 == 0) && c.sliding_window > 0 && S > c.sliding_window;
     const int  mask = swa ? 2 : 0;
 
+    // attention output: straight into the output projection's operand (s.xq) when the epilogue can
+    // quantise it, else f32 for acb_act_quant_ex
+    int     ao_type = ACB_TYPE_F32, ao_flags = 0;
+    int64_t ao_ts   = QD;
+    void *  ao      = att.p;
+    const bool fuse_o = dense_operand_spec(L.sa_o, exact, &ao_type, &ao_flags, &ao_ts);
+    if (fuse_o) {
+        ao = sc.xq;
+    } else {
+        ao_type = ACB_TYPE_F32;
+        ao_flags = 0;
+        ao_ts    = QD;
+    }
     // self-attention: adaLN (norm1, shift/scale_msa) inside the qkv projection's activation producer
     NormSpec ns_sa;
     ns_sa.w               = (const float *) L.sa_norm->data;
@@ -289,8 +302,8 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
                                         Nkv, (const float *) L.sa_k_norm->data, D, eps, pos.as<int32_t>(),
                                         rope.as<float>(), S, e, as));
         ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, vl, as));
-        ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, Ng, S, S, Nh, Nkv, D, mask,
-                            c.sliding_window, 0, scale, kPdl, lo, lo, vl, e, as));
+        ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
+                            c.sliding_window, 0, scale, kPdl | ao_flags, lo, lo, vl, e, as));
     } else {
         uint16_t * q16p = qkv16.as<uint16_t>();
         ACB_TRY(dense_forward(L.sa_qkv, false, hp, H, 0, R, q16p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
@@ -302,11 +315,15 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
                                  (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
                                  as));
         ACB_TRY(acb_attn_vt(q16p + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, 0, as));
-        ACB_TRY(acb_attn_tc(q16.p, QD, k16.p, KD, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, Ng, S, S, Nh, Nkv, D, mask,
-                            c.sliding_window, 0, scale, kPdl, 0, 0, 0, e, as));
+        ACB_TRY(acb_attn_tc(q16.p, QD, k16.p, KD, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
+                            c.sliding_window, 0, scale, kPdl | ao_flags, 0, 0, 0, e, as));
     }
-    ACB_TRY(dense_forward(L.sa_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0, R,
-                          sc, s));
+    if (fuse_o) {  // the attention wrote the output projection's operand
+        ACB_TRY(dense_forward_operand(L.sa_o, exact, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0, R, sc, s));
+    } else {
+        ACB_TRY(dense_forward(L.sa_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0,
+                              R, sc, s));
+    }
 
     // cross-attention over the cached condition K/V; norm2 inside the q projection's producer
     NormSpec ns_ca;
@@ -315,6 +332,17 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     float * cq = qkv32.as<float>();
     ACB_TRY(dense_forward(L.ca_q, exact, hp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc, s,
                           &ns_ca));
+    int     co_type = ACB_TYPE_F32, co_flags = 0;
+    int64_t co_ts   = QD;
+    void *  co      = att.p;
+    const bool fuse_co = dense_operand_spec(L.ca_o, exact, &co_type, &co_flags, &co_ts);
+    if (fuse_co) {
+        co = sc.xq;
+    } else {
+        co_type  = ACB_TYPE_F32;
+        co_flags = 0;
+        co_ts    = QD;
+    }
     const uint16_t * k_hi  = kvcache.as<uint16_t>() + (size_t) l * kv_layer_elems;
     const uint16_t * vt_hi = k_hi + 2 * k_plane;
     if (exact) {
@@ -322,16 +350,20 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
         uint16_t *    qh = planes.as<uint16_t>();
         ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, (const float *) L.ca_q_norm->data, 0,
                                         nullptr, D, eps, nullptr, nullptr, 0, e, as));
-        ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
-                            0, scale, kPdl, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
+        ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
+                            0, scale, kPdl | co_flags, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
     } else {
         ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
                                  (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
-        ACB_TRY(acb_attn_tc(q16.p, QD, k_hi, KD, vt_hi, enc_ld, att.p, ACB_TYPE_F32, QD, Ng, S, enc_S, Nh, Nkv, D, 0,
-                            0, 0, scale, kPdl, 0, 0, 0, e, as));
+        ACB_TRY(acb_attn_tc(q16.p, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0,
+                            0, 0, scale, kPdl | co_flags, 0, 0, 0, e, as));
     }
-    ACB_TRY(dense_forward(L.ca_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0,
-                          sc, s));
+    if (fuse_co) {
+        ACB_TRY(dense_forward_operand(L.ca_o, exact, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0, sc, s));
+    } else {
+        ACB_TRY(dense_forward(L.ca_o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
+                              0, sc, s));
+    }
 
     // FFN: adaLN (norm3, shift/scale_mlp) inside the gate/up projection's producer
     NormSpec ns_ff = ns_sa;

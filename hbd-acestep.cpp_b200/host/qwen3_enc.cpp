@@ -159,6 +159,18 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
     const int          mask  = c.is_causal ? 1 : 0;
     for (int l = l0; l < l1; l++) {
         const EncLayer & L = layers[(size_t) l];
+        // attention output straight into the output projection's operand when possible
+        int        ao_type = ACB_TYPE_F32, ao_flags = 0;
+        int64_t    ao_ts   = QD;
+        void *     ao      = att.p;
+        const bool fuse_o  = dense_operand_spec(L.o, exact, &ao_type, &ao_flags, &ao_ts);
+        if (fuse_o) {
+            ao = sc.xq;
+        } else {
+            ao_type  = ACB_TYPE_F32;
+            ao_flags = 0;
+            ao_ts    = QD;
+        }
         // input_layernorm inside the qkv projection's activation producer
         NormSpec ns_in;
         ns_in.w   = (const float *) L.attn_norm->data;
@@ -178,8 +190,8 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
                                             rope.as<float>(), cap, e, as));
             ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D, vtb.p, s_ld, vl,
                                 as));
-            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, 1, S, S, Nh, Nkv, D, mask, 0,
-                                0, scale, kPdl, lo, lo, vl, e, as));
+            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+                                scale, kPdl | ao_flags, lo, lo, vl, e, as));
         } else {
             ACB_TRY(dense_forward(L.qkv, false, hp, H, 0, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
                                   0, sc, s, &ns_in));
@@ -191,11 +203,15 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
                                      e, as));
             ACB_TRY(acb_attn_vt(qkv.as<uint16_t>() + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D,
                                 vtb.p, s_ld, 0, as));
-            ACB_TRY(acb_attn_tc(q.p, QD, k.p, KD, vtb.p, s_ld, att.p, ACB_TYPE_F32, QD, 1, S, S, Nh, Nkv, D, mask, 0, 0,
-                                scale, kPdl, 0, 0, 0, e, as));
+            ACB_TRY(acb_attn_tc(q.p, QD, k.p, KD, vtb.p, s_ld, ao, ao_type, ao_ts, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+                                scale, kPdl | ao_flags, 0, 0, 0, e, as));
         }
-        ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
-                              0, sc, s));
+        if (fuse_o) {  // the attention wrote the output projection's operand
+            ACB_TRY(dense_forward_operand(L.o, exact, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0, sc, s));
+        } else {
+            ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
+                                  0, sc, s));
+        }
         // post_attention_layernorm inside the gate/up projection's producer
         NormSpec ns_post;
         ns_post.w   = (const float *) L.post_norm->data;

@@ -151,7 +151,10 @@ ACB_API acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int ty
 /* ---- dense path (configs 1, 4, 5): tensor-core GEMM ---------------------------------------- */
 
 enum {
-    ACB_FLAG_F16 = 2, /* acb_gemm_bf16 / acb_attn_prefill: the tensor-core operands are f16, not bf16 */
+    ACB_FLAG_F16    = 2, /* acb_gemm_bf16 / acb_attn_prefill: the tensor-core operands are f16, not bf16 */
+    ACB_FLAG_GEMM_A = 4, /* acb_attn_tc with o_type Q8_0 / F16 / BF16: write the output projection's
+                            exact operand [hi | hi | lo] (hi at column c, again at Nh*128 + c, lo at
+                            2*Nh*128 + c; o_ts >= 3*Nh*128) instead of one 16-bit copy */
 };
 
 /* Activation operand of a tensor-core linear, with the arithmetic of ggml-CPU's quantised
@@ -291,9 +294,13 @@ ACB_API acb_status acb_attn_prefill_split(const void * q, int64_t q_bs, int64_t 
  * tiles, one softmax thread per query row): the same results as acb_attn_prefill for sequences
  * stored batch after batch. q [batch*Sq][q_ts] and k [batch*Skv][k_ts] f16 (head h at column
  * h*128; q_ts, k_ts multiples of 8); V is given transposed, vt [batch][Nkv][128][vt_ld] f16
- * (acb_attn_vt, vt_ld >= Skv, a multiple of 8); o [batch*Sq][o_ts] f32, bf16 or f16. With q_lo /
- * k_lo / vt_lo nonzero every operand has an f16 lo plane that many elements further and the
- * products are lo.hi + hi.lo + hi.hi: f32-accurate attention. Masks as acb_attn_prefill. */
+ * (acb_attn_vt, vt_ld >= Skv, a multiple of 8); o [batch*Sq][o_ts] f32, bf16 or f16, or o_type
+ * Q8_0: the output projection's activation operand (every 32 output columns quantised as one
+ * Q8_0 block the way ggml's from_float does, stored as f16 d*q; with ACB_FLAG_GEMM_A as the exact
+ * [hi|hi|lo] operand) -- the ggml_mul_mat(attn_o, .) input of src/dit-graph.h:236, 356 and
+ * src/qwen3-enc.h:201, identical to an f32 output followed by acb_act_quant_ex. With q_lo / k_lo
+ * / vt_lo nonzero every operand has an f16 lo plane that many elements further and the products
+ * are lo.hi + hi.lo + hi.hi: f32-accurate attention. Masks as acb_attn_prefill. */
 ACB_API acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, int64_t k_ts, const void * vt,
                                int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
                                int Nkv, int head_dim, int mask, int window, int causal_off, float scale, int flags,

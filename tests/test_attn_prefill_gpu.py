@@ -189,3 +189,32 @@ def test_attn_tc_matches_reference(cuda, B, Sq, Skv, Nh, Nkv, mask, window, caus
         hv = vp[: B * Skv].view(B, Skv, -1)
         o3 = acb.attn_prefill_split(hq, hk, hv, qlo, klo, v.numel(), Nh, Nkv, mask=mask, window=window)
         assert max_rel(o2.view(B, Sq, -1).cpu().numpy(), o3.cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("split,gemm_a,quant", [(True, True, O.Q8_0), (False, False, O.Q8_0), (True, True, O.F16),
+                                                (False, False, O.BF16)])
+def test_attn_tc_quantised_output(cuda, split, gemm_a, quant):
+    """acb_attn_tc writing the output projection's operand (o_type Q8_0 / F16 / BF16, optionally the
+    exact [hi|hi|lo] layout) == the f32 output followed by acb_act_quant_ex, bit for bit."""
+    import torch
+    B, Sq, Skv, Nh, Nkv = 2, 300, 200, 4, 2
+    g = torch.Generator(device=cuda).manual_seed(77 + split)
+    q = torch.randn(B * Sq, Nh * 128, device=cuda, generator=g)
+    k = torch.randn(B * Skv, Nkv * 128, device=cuda, generator=g)
+    v = torch.randn(B, Skv, Nkv * 128, device=cuda, generator=g)
+    if split:
+        qp = acb.act_quant_ex(q, Nh * 128, acb.F16, acb.LAYOUT_PLANES)
+        kp = acb.act_quant_ex(k, Nkv * 128, acb.F16, acb.LAYOUT_PLANES)
+        vt, ld, vlo = acb.attn_vt(v, Nkv, lo=True)
+        lo = dict(q_lo=q.numel(), k_lo=k.numel(), vt_lo=vlo)
+        qq, kk = qp[: B * Sq], kp[: B * Skv]
+    else:
+        vt, ld, _ = acb.attn_vt(v.half(), Nkv)
+        lo = {}
+        qq, kk = q.half(), k.half()
+    o32 = acb.attn_tc(qq, kk, vt, ld, Nh, Nkv, Sq, Skv, B, **lo)
+    got = acb.attn_tc(qq, kk, vt, ld, Nh, Nkv, Sq, Skv, B, quant=quant, gemm_a=gemm_a, **lo)
+    layout = acb.LAYOUT_GEMM_A if gemm_a else acb.LAYOUT_PLAIN
+    want = acb.act_quant_ex(o32, Nh * 128, quant, layout)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
