@@ -127,9 +127,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t * v_full   = k_empty + Lay::NK;
     uint64_t * v_empty  = v_full + Lay::NV;
     uint64_t * s_full   = v_empty + Lay::NV;
-    uint64_t * p_full   = s_full + 2;
-    uint64_t * pv_done  = p_full + 1;
-    uint64_t * xbar     = pv_done + 1;  // [4]: softmax pair exchange, one per TMEM lane quarter
+    uint64_t * p_full   = s_full + 2;   // [2]: P of block i is published on p_full[i & 1] (a softmax
+                                        // warp may run one block ahead of the slowest)
+    uint64_t * pv_done  = p_full + 2;   // [2]: P.V of block i completes on pv_done[i & 1]
+    uint64_t * o_done   = pv_done + 2;  // the last P.V has completed
+    uint64_t * xbar     = o_done + 1;   // [4]: softmax pair exchange, one per TMEM lane quarter
     uint32_t * tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
     __shared__ volatile int abort_flag;
     __shared__ float        xchg[2 * 2 * kTcBQ];  // softmax pair exchange: [parity][half][row]
@@ -163,8 +165,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         ptx::mbar_init(&s_full[0], 1);
         ptx::mbar_init(&s_full[1], 1);
-        ptx::mbar_init(p_full, 8);  // one arrival per softmax warp
-        ptx::mbar_init(pv_done, 1);
+        ptx::mbar_init(&p_full[0], 8);  // one arrival per softmax warp
+        ptx::mbar_init(&p_full[1], 8);
+        ptx::mbar_init(&pv_done[0], 1);
+        ptx::mbar_init(&pv_done[1], 1);
+        ptx::mbar_init(o_done, 1);
         for (int x = 0; x < 4; x++) {
             ptx::mbar_init(&xbar[x], 2);  // the two warps of a pair
         }
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             };
             bool ok = issue_s(0) && (nblk < 2 || issue_s(1));
             for (int i = 0; ok && i < nblk; i++) {
-                if (!tc_wait(p_full, i & 1, &abort_flag, a.err)) {
+                if (!tc_wait(&p_full[i & 1], (i >> 1) & 1, &abort_flag, a.err)) {
                     break;
                 }
                 const int sv = i % Lay::NV;
@@ -269,8 +274,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         acc = 1;
                     }
                 }
-                umma_commit(pv_done);
+                umma_commit(&pv_done[i & 1]);
                 umma_commit(&v_empty[sv]);  // this V block is consumed
+                if (i + 1 == nblk) {
+                    umma_commit(o_done);
+                }
                 if (i + 2 < nblk) {
                     ok = issue_s(i + 2);
                 }
@@ -330,6 +338,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 return false;
             }
             *other = xchg[((phase & 1) * 2 + (hf ^ 1)) * kTcBQ + row];
+            return true;
+        };
+        // P.V(k) has completed: pv_done[k & 1], phase k >> 1 (waited in order, one phase at a time)
+        int  pv_seen[2] = { 0, 0 };
+        auto wait_pv    = [&](int k) -> bool {
+            const int bb = k & 1, ph = k >> 1;
+            if (pv_seen[bb] > ph) {
+                return true;
+            }
+            if (!__all_sync(0xffffffffu, tc_wait(&pv_done[bb], ph & 1, &abort_flag, a.err))) {
+                return false;
+            }
+            pv_seen[bb] = ph + 1;
+            tc_fence_after();
             return true;
         };
         for (int i = 0; i < nblk; i++) {
@@ -422,25 +444,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 ph[e] = r[2 * e];
                 pl[e] = r[2 * e + 1];
             }
-            if (i > 0) {
-                // the previous P.V has finished: O may be rescaled
-                if (!__all_sync(0xffffffffu, tc_wait(pv_done, (i - 1) & 1, &abort_flag, a.err))) {
+            // P.V(i-2) has completed (S(i), already seen, follows it in the in-order tensor pipe):
+            // record it, so that every pv_done barrier is waited at most one phase behind
+            if (i >= 2 && !wait_pv(i - 2)) {
+                ok = false;
+                break;
+            }
+            if (__any_sync(0xffffffffu, resc)) {
+                // rescaling O needs P.V(i-1) finished; otherwise P(i) goes out without waiting
+                if (!wait_pv(i - 1)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-                    for (int c = 0; c < 2; c++) {
-                        uint32_t       o[32];
-                        const uint32_t col = (uint32_t) (hf * 64 + c * 32);
-                        tmem_ld32(tO + lanes + col, o);
+                for (int c = 0; c < 2; c++) {
+                    uint32_t       o[32];
+                    const uint32_t col = (uint32_t) (hf * 64 + c * 32);
+                    tmem_ld32(tO + lanes + col, o);
 #pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        }
-                        tmem_st32(tO + lanes + col, o);
+                    for (int e = 0; e < 32; e++) {
+                        o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
                     }
+                    tmem_st32(tO + lanes + col, o);
                 }
             }
             l = l * alpha + ls;
@@ -453,11 +478,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                ptx::mbar_arrive(p_full);
+                ptx::mbar_arrive(&p_full[i & 1]);
             }
         }
         if (ok && nblk > 0) {
-            ok = __all_sync(0xffffffffu, tc_wait(pv_done, (nblk - 1) & 1, &abort_flag, a.err));
+            ok = __all_sync(0xffffffffu, tc_wait(o_done, 0, &abort_flag, a.err));
             tc_fence_after();
         }
         // row sum of both halves (exchange slot nblk & 1 is free: the last exchange used the other)
