@@ -7,9 +7,9 @@
 // O accumulator and Q (P and Q are the A operands of the two products, two f16 per 32-bit column),
 // so the tensor cores read only K and V from shared memory, and every MMA is N = 128 wide (the
 // narrower N = 64 form runs at about two thirds of the tensor rate):
-//   warp 0      TMA: key blocks of 128, K [128][128] and V^T [128][128], into separate rings (a K
-//               stage is released as soon as its scores are computed, a V stage after P.V),
-//               128-byte swizzled K-major tiles;
+//   warp 0      TMA, two threads: key blocks of 128, K [128][128] and V^T [128][128], into separate
+//               rings (a K stage is released as soon as its scores are computed, a V stage after
+//               P.V; neither stream waits on the other), 128-byte swizzled K-major tiles;
 //   warp 1      one thread issues tcgen05.mma with A from TMEM: S = Q.K^T (M=128 queries, N=128
 //               keys) into one of the two S/P buffers, and O += P.V (M=128, N=128 head dims); S for
 //               block i+2 is issued right after P.V of block i (the tensor pipe runs them in order,
@@ -191,10 +191,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t tQ   = tmem + Lay::TQ;
 
     if (warp == 0) {
+        // two independent producer threads: lane 0 streams K blocks (a stage frees as soon as its
+        // scores are computed), lane 16 streams V^T blocks (a stage frees after its P.V)
         if (lane == 0 && nblk > 0) {
             for (int i = 0; i < nblk; i++) {
                 const int key0 = (kb_lo + i) * kTcBK;
-                const int sk = i % Lay::NK, sv = i % Lay::NV;
+                const int sk   = i % Lay::NK;
                 if (i >= Lay::NK && !tc_wait(&k_empty[sk], ((i / Lay::NK) - 1) & 1, &abort_flag, a.err)) {
                     break;
                 }
@@ -206,6 +208,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                     &k_full[sk]);
                     }
                 }
+            }
+        } else if (lane == 16 && nblk > 0) {
+            for (int i = 0; i < nblk; i++) {
+                const int key0 = (kb_lo + i) * kTcBK;
+                const int sv   = i % Lay::NV;
                 if (i >= Lay::NV && !tc_wait(&v_empty[sv], ((i / Lay::NV) - 1) & 1, &abort_flag, a.err)) {
                     break;
                 }
