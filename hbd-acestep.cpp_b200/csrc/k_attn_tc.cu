@@ -42,9 +42,6 @@ constexpr int kTcThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
 enum { TC_MASK_NONE = 0, TC_MASK_CAUSAL = 1, TC_MASK_WINDOW = 2 };
 
 struct AttnTcArgs {
-    const uint16_t * q;     // Q hi plane: element (b, i, h, d) at (b*Sq + i)*q_ts + h*128 + d
-    int64_t          q_ts;
-    int64_t          q_lo;  // lo plane offset (elements)
     void *  o;
     int     o_type;
     int64_t o_ts;  // O element (b, i, h, d) at (b*Sq + i)*o_ts + h*128 + d
@@ -62,7 +59,9 @@ template <bool SPLIT> struct TcLayout {
     static constexpr int VB    = NP * 2 * 16384;      // V^T block: plane x key-chunk x [128 d][64 keys]
     static constexpr int NK    = SPLIT ? 2 : 3;       // K ring stages
     static constexpr int NV    = SPLIT ? 1 : 2;       // V ring stages
+    static constexpr int QB    = NP * 2 * 16384;      // Q tile: plane x d-chunk x [128 q][64 d]
     static constexpr int TOTAL = NK * KB + NV * VB;   // 192 KB split, 160 KB otherwise
+    static_assert(QB <= VB, "the Q tile is staged in V stage 0");
     // TMEM columns (512 allocated): two S/P buffers of 128 columns (S fp32; after the softmax, P
     // as f16 pairs: hi plane in the first 64 columns, lo plane in the next 64), O at 256..383,
     // Q planes (64 columns each: two f16 per column) from 384
@@ -113,7 +112,8 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t * r) {
 
 template <int MASK, bool SPLIT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mkl,
+    attn_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mql,
+                   const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mkl,
                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mvl,
                    const AttnTcArgs a) {
     using Lay = TcLayout<SPLIT>;
@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t * sK   = smem;
     uint8_t * sV   = sK + Lay::NK * Lay::KB;
     uint64_t * q_full   = reinterpret_cast<uint64_t *>(sV + Lay::NV * Lay::VB);
-    uint64_t * k_full   = q_full + 1;
+    uint64_t * q_tma    = q_full + 1;  // the Q tile has landed in V stage 0
+    uint64_t * k_full   = q_tma + 1;
     uint64_t * k_empty  = k_full + Lay::NK;
     uint64_t * v_full   = k_empty + Lay::NK;
     uint64_t * v_empty  = v_full + Lay::NV;
@@ -155,6 +156,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) {
         abort_flag = 0;
         ptx::mbar_init(q_full, 8);  // one arrival per softmax warp once its Q columns are in TMEM
+        ptx::mbar_init(q_tma, 1);
         for (int s = 0; s < Lay::NK; s++) {
             ptx::mbar_init(&k_full[s], 1);
             ptx::mbar_init(&k_empty[s], 1);
@@ -174,6 +176,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ptx::mbar_init(&xbar[x], 2);  // the two warps of a pair
         }
         ptx::fence_mbar_init();
+        tma_prefetch_desc(&mq);
         tma_prefetch_desc(&mk);
         tma_prefetch_desc(&mv);
     }
@@ -210,7 +213,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
         } else if (lane == 16 && nblk > 0) {
-            for (int i = 0; i < nblk; i++) {
+            // the Q tile (both planes, 64 KB split / 32 KB) goes through V stage 0 on its way to TMEM
+            ptx::mbar_arrive_expect_tx(q_tma, Lay::QB);
+            for (int p = 0; p < Lay::NP; p++) {
+                for (int c = 0; c < 2; c++) {
+                    tma_load_2d(sV + (p * 2 + c) * 16384, p ? &mql : &mq, h * kTcD + c * 64, b * a.Sq + q0, q_tma);
+                }
+            }
+            const bool q_copied = tc_wait(q_full, 0, &abort_flag, a.err);
+            for (int i = 0; q_copied && i < nblk; i++) {
                 const int key0 = (kb_lo + i) * kTcBK;
                 const int sv   = i % Lay::NV;
                 if (i >= Lay::NV && !tc_wait(&v_empty[sv], ((i / Lay::NV) - 1) & 1, &abort_flag, a.err)) {
@@ -304,27 +315,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t lanes = (uint32_t) (qq * 32) << 16;
         float          m = -INFINITY, l = 0.0f;
         bool           ok = true;
-        // this row's Q (dims [64 hf, 64 hf + 64) of each plane) into TMEM: 32 columns per plane
-        {
-            const uint16_t * qr = a.q + ((int64_t) b * a.Sq + iq) * a.q_ts + (int64_t) h * kTcD + hf * 64;
-#pragma unroll 1
+        // this row's Q (dims [64 hf, 64 hf + 64) of each plane) from the swizzled TMA tile in V stage
+        // 0 into TMEM, 32 columns per plane (16-byte unit u of row r sits at unit u ^ (r % 8))
+        if (nblk == 0) {
+            // no key block: nothing to stage (the output rows are zero)
+        } else if (__all_sync(0xffffffffu, tc_wait(q_tma, 0, &abort_flag, a.err))) {
+#pragma unroll
             for (int p = 0; p < Lay::NP; p++) {
-                uint32_t v[32];
-                if (iq < a.Sq) {
-                    const uint4 * src = reinterpret_cast<const uint4 *>(qr + (p ? a.q_lo : 0));
+                const uint8_t * src = sV + (p * 2 + hf) * 16384 + row * 128;
+                uint32_t        v[32];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        const uint4 t = src[e];
-                        v[4 * e]      = t.x;
-                        v[4 * e + 1]  = t.y;
-                        v[4 * e + 2]  = t.z;
-                        v[4 * e + 3]  = t.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        v[e] = 0u;
-                    }
+                for (int u = 0; u < 8; u++) {
+                    const uint4 t = *reinterpret_cast<const uint4 *>(src + ((u ^ (row & 7)) << 4));
+                    v[4 * u]      = t.x;
+                    v[4 * u + 1]  = t.y;
+                    v[4 * u + 2]  = t.z;
+                    v[4 * u + 3]  = t.w;
                 }
                 tmem_st32(tQ + lanes + (uint32_t) (p * 64 + hf * 32), v);
             }
@@ -333,6 +339,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (lane == 0) {
                 ptx::mbar_arrive(q_full);
             }
+        } else {
+            ok = false;
         }
         // publish v for `phase`, wait for the partner (bounded), return its value
         auto pair_xchg = [&](int phase, float v, float * other) -> bool {
@@ -348,16 +356,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             return true;
         };
         // P.V(k) has completed: pv_done[k & 1], phase k >> 1 (waited in order, one phase at a time)
-        int  pv_seen[2] = { 0, 0 };
-        auto wait_pv    = [&](int k) -> bool {
+        int  pv_seen0 = 0, pv_seen1 = 0;  // phases of pv_done[0] / pv_done[1] waited
+        auto wait_pv  = [&](int k) -> bool {
             const int bb = k & 1, ph = k >> 1;
-            if (pv_seen[bb] > ph) {
+            int &     seen = bb ? pv_seen1 : pv_seen0;
+            if (seen > ph) {
                 return true;
             }
             if (!__all_sync(0xffffffffu, tc_wait(&pv_done[bb], ph & 1, &abort_flag, a.err))) {
                 return false;
             }
-            pv_seen[bb] = ph + 1;
+            seen = ph + 1;
             tc_fence_after();
             return true;
         };
@@ -499,82 +508,102 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         const float lt  = ok ? l + lo_sum : 0.0f;
         const float inv = (ok && lt > 0.0f) ? 1.0f / lt : 0.0f;
+        // O rows through this warp's staging block in the (now idle) K ring, then written as whole
+        // row segments: f32, or 16-bit (Q8_0: each 32 columns one block of the output projection's
+        // quantised operand, ggml from_float: d = amax / 127 stored as f16, q = round(y / d))
+        const int sw  = warp - 2;  // 0..7: rows 32 (w % 4) .. +31, columns 64 hf .. +63
+        uint8_t * stg = sK + sw * 9216;
+        const bool f32o = a.o_type == ACB_TYPE_F32, bfo = a.o_type == ACB_TYPE_BF16;
 #pragma unroll 1
         for (int c = 0; c < 2; c++) {
-            const int col = hf * 64 + c * 32;
-            uint32_t  o[32];
+            uint32_t o[32];
             if (nblk > 0 && ok) {
-                tmem_ld32(tO + lanes + (uint32_t) col, o);
+                tmem_ld32(tO + lanes + (uint32_t) (hf * 64 + c * 32), o);
             } else {
 #pragma unroll
                 for (int e = 0; e < 32; e++) {
                     o[e] = 0u;
                 }
             }
-            if (iq < a.Sq) {
-                const int64_t base = ((int64_t) b * a.Sq + iq) * a.o_ts + (int64_t) h * kTcD + col;
-                if (a.o_type == ACB_TYPE_F32) {
-                    float4 * d = reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.o) + base);
+            float y[32];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        d[e] = make_float4(__uint_as_float(o[4 * e]) * inv, __uint_as_float(o[4 * e + 1]) * inv,
-                                           __uint_as_float(o[4 * e + 2]) * inv, __uint_as_float(o[4 * e + 3]) * inv);
+            for (int e = 0; e < 32; e++) {
+                y[e] = __uint_as_float(o[e]) * inv;
+            }
+            if (f32o) {  // [32 rows][64 f32 + 4 pad]
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    *reinterpret_cast<float4 *>(stg + lane * 272 + (c * 32 + e) * 4) =
+                        make_float4(y[e], y[e + 1], y[e + 2], y[e + 3]);
+                }
+                continue;
+            }
+            if (a.o_type == ACB_TYPE_Q8_0) {
+                float amax = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    amax = fmaxf(amax, fabsf(y[e]));
+                }
+                const float d  = __fdiv_rn(amax, 127.0f);
+                const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+                const float dh = __half2float(__float2half_rn(d));
+#pragma unroll
+                for (int e = 0; e < 32; e++) {
+                    y[e] = __fmul_rn(dh, (float) (int) roundf(__fmul_rn(y[e], id)));
+                }
+            }
+            // hi plane [32 rows][64 x 16-bit + 8 pad] at 0, lo plane at 4608
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float v0 = y[e + 2 * j], v1 = y[e + 2 * j + 1];
+                    if (bfo) {
+                        __nv_bfloat162 bb = __floats2bfloat162_rn(v0, v1);
+                        const float2   f2 = __bfloat1622float2(bb);
+                        __nv_bfloat162 ll = __floats2bfloat162_rn(__fsub_rn(v0, f2.x), __fsub_rn(v1, f2.y));
+                        hw[j]             = *reinterpret_cast<uint32_t *>(&bb);
+                        lw[j]             = *reinterpret_cast<uint32_t *>(&ll);
+                    } else {
+                        __half2      hh = __floats2half2_rn(v0, v1);
+                        const float2 f2 = __half22float2(hh);
+                        __half2      ll = __floats2half2_rn(__fsub_rn(v0, f2.x), __fsub_rn(v1, f2.y));
+                        hw[j]           = *reinterpret_cast<uint32_t *>(&hh);
+                        lw[j]           = *reinterpret_cast<uint32_t *>(&ll);
                     }
-                } else {
-                    // 16-bit output; Q8_0: these 32 columns are one block of the output projection's
-                    // quantised operand (ggml from_float: d = amax / 127 stored as f16, q = round(y / d))
-                    float y[32];
-#pragma unroll
-                    for (int e = 0; e < 32; e++) {
-                        y[e] = __uint_as_float(o[e]) * inv;
-                    }
-                    if (a.o_type == ACB_TYPE_Q8_0) {
-                        float amax = 0.0f;
-#pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            amax = fmaxf(amax, fabsf(y[e]));
-                        }
-                        const float d  = __fdiv_rn(amax, 127.0f);
-                        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-                        const float dh = __half2float(__float2half_rn(d));
-#pragma unroll
-                        for (int e = 0; e < 32; e++) {
-                            y[e] = __fmul_rn(dh, (float) (int) roundf(__fmul_rn(y[e], id)));
-                        }
-                    }
-                    const bool bfo = a.o_type == ACB_TYPE_BF16;
-                    uint32_t   pk[16], pl[16];
-#pragma unroll
-                    for (int e = 0; e < 16; e++) {
-                        const float v0 = y[2 * e], v1 = y[2 * e + 1];
-                        if (bfo) {
-                            __nv_bfloat162 bb = __floats2bfloat162_rn(v0, v1);
-                            pk[e]             = *reinterpret_cast<uint32_t *>(&bb);
-                            const float2 f2   = __bfloat1622float2(bb);
-                            __nv_bfloat162 ll = __floats2bfloat162_rn(__fsub_rn(v0, f2.x), __fsub_rn(v1, f2.y));
-                            pl[e]             = *reinterpret_cast<uint32_t *>(&ll);
-                        } else {
-                            __half2 hh      = __floats2half2_rn(v0, v1);
-                            pk[e]           = *reinterpret_cast<uint32_t *>(&hh);
-                            const float2 f2 = __half22float2(hh);
-                            __half2 ll      = __floats2half2_rn(__fsub_rn(v0, f2.x), __fsub_rn(v1, f2.y));
-                            pl[e]           = *reinterpret_cast<uint32_t *>(&ll);
-                        }
-                    }
-                    uint16_t * ob = reinterpret_cast<uint16_t *>(a.o) + base;
-                    uint4 *    d  = reinterpret_cast<uint4 *>(ob);
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        d[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-                    }
-                    if (a.gemm_a) {
-                        uint4 * d1 = reinterpret_cast<uint4 *>(ob + a.o_k);
-                        uint4 * d2 = reinterpret_cast<uint4 *>(ob + 2 * a.o_k);
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            d1[e] = make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
-                            d2[e] = make_uint4(pl[4 * e], pl[4 * e + 1], pl[4 * e + 2], pl[4 * e + 3]);
-                        }
+                }
+                const int off = lane * 144 + (c * 32 + e) * 2;
+                *reinterpret_cast<uint4 *>(stg + off)        = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *reinterpret_cast<uint4 *>(stg + 4608 + off) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
+        }
+        __syncwarp();
+        const int64_t row0 = (int64_t) b * a.Sq + q0 + qq * 32;  // global row of this warp's first row
+        const int     rmax = a.Sq - (q0 + qq * 32);               // rows of this warp inside the sequence
+        const int64_t col0 = (int64_t) h * kTcD + hf * 64;
+        if (f32o) {
+            // 16 lanes x 16 bytes per row, 2 rows per pass
+#pragma unroll 4
+            for (int it = 0; it < 16; it++) {
+                const int rr = it * 2 + (lane >> 4), cc = (lane & 15) * 4;
+                if (rr < rmax) {
+                    *reinterpret_cast<float4 *>(reinterpret_cast<float *>(a.o) + (row0 + rr) * a.o_ts + col0 + cc) =
+                        *reinterpret_cast<const float4 *>(stg + rr * 272 + cc * 4);
+                }
+            }
+        } else {
+            // 8 lanes x 16 bytes per row, 4 rows per pass; GEMM_A: hi twice, then lo
+            const int nplanes = a.gemm_a ? 3 : 1;
+            for (int pl = 0; pl < nplanes; pl++) {
+                const int src_off = pl == 2 ? 4608 : 0;
+                const int64_t dc  = col0 + (int64_t) pl * a.o_k;
+#pragma unroll 4
+                for (int it = 0; it < 8; it++) {
+                    const int rr = it * 4 + (lane >> 3), cc = (lane & 7) * 8;
+                    if (rr < rmax) {
+                        *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(a.o) + (row0 + rr) * a.o_ts + dc + cc) =
+                            *reinterpret_cast<const uint4 *>(stg + src_off + rr * 144 + cc * 2);
                     }
                 }
             }
@@ -674,14 +703,17 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     const uint16_t * q16 = reinterpret_cast<const uint16_t *>(q);
     const uint16_t * k16 = reinterpret_cast<const uint16_t *>(k);
     const uint16_t * v16 = reinterpret_cast<const uint16_t *>(vt);
-    CUtensorMap      mk, mkl, mv, mvl;
+    CUtensorMap      mq, mql, mk, mkl, mv, mvl;
     const int64_t    kc = (int64_t) Nkv * kTcD;
-    bool ok = make_map_2d(&mk, k16, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
+    bool ok = make_map_2d(&mq, q16, true, (int64_t) Nh * kTcD, (int64_t) batch * Sq, q_ts, 64, kTcBQ) &&
+              make_map_2d(&mk, k16, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
               make_map_2d(&mv, v16, true, Skv, (int64_t) batch * Nkv * kTcD, vt_ld, 64, kTcD);
     if (split) {
-        ok = ok && make_map_2d(&mkl, k16 + k_lo, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
+        ok = ok && make_map_2d(&mql, q16 + q_lo, true, (int64_t) Nh * kTcD, (int64_t) batch * Sq, q_ts, 64, kTcBQ) &&
+             make_map_2d(&mkl, k16 + k_lo, true, kc, (int64_t) batch * Skv, k_ts, 64, kTcBK) &&
              make_map_2d(&mvl, v16 + vt_lo, true, Skv, (int64_t) batch * Nkv * kTcD, vt_ld, 64, kTcD);
     } else {
+        mql = mq;
         mkl = mk;
         mvl = mv;
     }
@@ -689,9 +721,6 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
         return ACB_ERR_CUDA;
     }
     AttnTcArgs a = {};
-    a.q          = q16;
-    a.q_ts       = q_ts;
-    a.q_lo       = q_lo;
     a.o          = o;
     a.o_type     = o_type;
     a.o_ts       = o_ts;
@@ -706,8 +735,8 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     a.gemm_a     = gemm_a ? 1 : 0;
     a.o_k        = (int64_t) Nh * kTcD;
     const size_t smem = (size_t) (split ? TcLayout<true>::TOTAL : TcLayout<false>::TOTAL) + 1024 + 256;
-    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const AttnTcArgs) =
-        nullptr;
+    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                 const CUtensorMap, const AttnTcArgs) = nullptr;
 #define ACB_TC_PICK(M) kern = split ? attn_tc_kernel<M, true> : attn_tc_kernel<M, false>
     if (mask == TC_MASK_CAUSAL) {
         ACB_TC_PICK(TC_MASK_CAUSAL);
@@ -728,7 +757,7 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = (flags & ACB_FLAG_PDL) ? attr : nullptr;
     cfg.numAttrs                                       = (flags & ACB_FLAG_PDL) ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mk, mkl, mv, mvl, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mq, mql, mk, mkl, mv, mvl, a);
     if (e != cudaSuccess) {
         set_last_cuda_error(e);
         return ACB_ERR_CUDA;
