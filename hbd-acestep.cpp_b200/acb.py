@@ -125,6 +125,8 @@ def lib():
             "acb_vec_dot_type": (I, [I]),
             "acb_gemm_workspace_bytes": (C.c_size_t, [I64, I64, I64]),
             "acb_gemm_swiglu_quant": (I, [P, I64, P, I64, I64, I64, I64, P, I, I, P, I, I64, I, P, P]),
+            "acb_gemm_qkv_planes": (I, [P, I64, P, I64, I64, I64, I, I, P, P, F, P, P, I, I64, P, I64, I64, P, I64, I64,
+                                        I, P, P]),
             "acb_gemm_pair_clusters": (I, [I]),
             "acb_gemm_tc": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, C.c_size_t, P,
                                 P]),
@@ -420,6 +422,26 @@ def gemm_swiglu_quant(A, B, F, vec_type, layout, bias=None, err=None, stream=Non
         _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, F, K, _ptr(bias), vec_type, layout, _ptr(out), dtype_id(out),
         width, flags, _ptr(err), _stream(stream)))
     return out
+
+
+def gemm_qkv_planes(A, B, nq, nk, q_w, k_w, eps, seq, pos=None, rope=None, lo=True, err=None, stream=None):
+    """acb_gemm_qkv_planes: A [M, K], B [(nq + 2 nk)*128, K] 16-bit -> (qk planes [2M or M, (nq+nk)*128] f16,
+    vt planes from the V heads as acb_attn_vt lays them out, vt_ld, vt lo offset)."""
+    import torch
+    M, K = A.shape
+    W = (nq + nk) * 128
+    qk = torch.empty((2 * M if lo else M, W), dtype=torch.float16, device=A.device)
+    B_ = M // seq
+    vt_ld = (seq + 7) // 8 * 8
+    vt_plane = B_ * nk * 128 * vt_ld
+    vt = torch.zeros((2 * vt_plane if lo else vt_plane,), dtype=torch.float16, device=A.device)
+    max_pos = rope.shape[0] if rope is not None else 0
+    flags = FLAG_F16 if A.dtype == torch.float16 else 0
+    _check("acb_gemm_qkv_planes", lib().acb_gemm_qkv_planes(
+        _ptr(A), A.stride(0), _ptr(B), B.stride(0), M, K, nq, nk, _ptr(q_w), _ptr(k_w), eps, _ptr(pos), _ptr(rope),
+        max_pos, seq, _ptr(qk), W, M * W if lo else 0, _ptr(vt), vt_ld, vt_plane if lo else 0, flags, _ptr(err),
+        _stream(stream)))
+    return qk, vt, vt_ld, (vt_plane if lo else 0)
 
 
 def gemm_workspace_bytes(M, N, K) -> int:

@@ -68,6 +68,21 @@ struct GemmArgs {
     // sw_layout (PLAIN [M][F] or GEMM_A [M][3F]), 16-bit, ldc elements per row
     int           swiglu, sw_vt, sw_layout;
     int64_t       F;
+    // QKV epilogue (qkv != 0): output columns are nq q heads, nk k heads, then nk v heads of 128;
+    // q/k heads get RMSNorm (qn / kn) and, with a rope table, NeoX RoPE at pos[m], and go to the
+    // f16 planes qk [M][qk_ld] (hi; lo qk_lo elements further when nonzero); v heads go transposed
+    // to vt[((b*nk + hv)*128 + d)*vt_ld + t] (m = b*seq + t; lo vt_lo further when nonzero)
+    int             qkv, nq, nk, max_pos;
+    const float *   qn;
+    const float *   kn;
+    float           eps;
+    const int32_t * pos;
+    const float *   rope;
+    int64_t         seq;
+    uint16_t *      qk;
+    int64_t         qk_ld, qk_lo;
+    uint16_t *      vt;
+    int64_t         vt_ld, vt_lo;
     int           group_m;  // tile order: groups of group_m m-tiles, n-tiles outer within a group, m inner
     int           splits;  // split-K factor; > 1: raw partials to ws, epilogue by splitk_reduce_kernel
     int           kps;     // k-tiles per split
@@ -220,6 +235,172 @@ __device__ __forceinline__ void tile_mn(int64_t t, int64_t m_tiles, int64_t n_ti
     const int64_t gm  = m_tiles - m0 < group_m ? m_tiles - m0 : group_m;
     mt                = m0 + idx % gm;
     nt                = idx / gm;
+}
+
+// 32 values per row of this warp's 32 rows (lane = row m_base + lane, values v) as f16 at
+// base + m*ld + col: the high parts, or with LO the low parts f16(v - f16(v)); staged through
+// shared memory (20 words per row) so that each row's 64 bytes are written by 4 lanes.
+template <bool LO>
+__device__ __forceinline__ void put_rows32_f16(uint32_t * sw, int lane, const float * v, uint16_t * base, int64_t ld,
+                                               int64_t m_base, int64_t M, int64_t col) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        uint32_t wv[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float a = v[j + 2 * e], b = v[j + 2 * e + 1];
+            __half2     hh = __floats2half2_rn(a, b);
+            if (LO) {
+                const float2 f2 = __half22float2(hh);
+                hh              = __floats2half2_rn(__fsub_rn(a, f2.x), __fsub_rn(b, f2.y));
+            }
+            wv[e] = *reinterpret_cast<uint32_t *>(&hh);
+        }
+        *reinterpret_cast<uint4 *>(sw + lane * 20 + j / 2) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+        const int     rr = it * 8 + (lane >> 2), part = lane & 3;
+        const int64_t mr = m_base + rr;
+        if (mr < M) {
+            *reinterpret_cast<uint4 *>(base + mr * ld + col + part * 8) =
+                *reinterpret_cast<const uint4 *>(sw + rr * 20 + part * 4);
+        }
+    }
+    __syncwarp();
+}
+
+// QKV epilogue of one warp: rows m_base + lane, output columns n0 .. n0 + 255 = two heads. For a q
+// or k head: RMSNorm with the sum of squares in the association order of the one-warp-per-head
+// kernel (lane l's partial ((a[2l]^2 + a[2l+1]^2) + b[2l]^2) + b[2l+1]^2 in double, a = dims
+// 0..63, b = 64..127, then the xor-butterfly tree), so the result is bit-identical to
+// acb_qk_norm_rope_planes over the f32 product; then NeoX RoPE and the hi/lo planes. A v head
+// goes to the transposed planes, 32 tokens per store (one dim).
+__device__ __forceinline__ void qkv_epilogue(const GemmArgs & g, uint32_t tacc, int64_t m_base, int64_t n0, int lane,
+                                             float * stg) {
+    const int64_t m  = m_base + lane;
+    uint32_t *    sw = reinterpret_cast<uint32_t *>(stg);
+    int           p  = 0;
+    if (g.rope && m < g.M) {
+        p = __ldg(g.pos + m);
+        if (p < 0 || p >= g.max_pos) {
+            if (g.err) {
+                atomicOr(g.err, ACB_DEVERR_POS_RANGE);
+            }
+            p = -1;  // this row is written as zeros
+        }
+    }
+#pragma unroll 1
+    for (int hh = 0; hh < 2; hh++) {
+        const int      hd  = (int) (n0 / 128) + hh;
+        const uint32_t tc0 = tacc + (uint32_t) (hh * 128);
+        if (hd < g.nq + g.nk) {
+            const float * w = hd < g.nq ? g.qn : g.kn;
+            float         sc = 1.0f;
+            if (w) {
+                uint32_t ra[32], rb[32];
+                double   t[16];
+                tmem_ld32(tc0 + 0, ra);   // dims 0..31   (lanes 0..15 of the per-head kernel)
+                tmem_ld32(tc0 + 64, rb);  // dims 64..95
+#pragma unroll
+                for (int l = 0; l < 16; l++) {
+                    const float a0 = __uint_as_float(ra[2 * l]), a1 = __uint_as_float(ra[2 * l + 1]);
+                    const float b0 = __uint_as_float(rb[2 * l]), b1 = __uint_as_float(rb[2 * l + 1]);
+                    double      s  = (double) __fmul_rn(a0, a0);
+                    s += (double) __fmul_rn(a1, a1);
+                    s += (double) __fmul_rn(b0, b0);
+                    s += (double) __fmul_rn(b1, b1);
+                    t[l] = s;
+                }
+                tmem_ld32(tc0 + 32, ra);  // dims 32..63  (lanes 16..31)
+                tmem_ld32(tc0 + 96, rb);  // dims 96..127
+#pragma unroll
+                for (int l = 0; l < 16; l++) {
+                    const float a0 = __uint_as_float(ra[2 * l]), a1 = __uint_as_float(ra[2 * l + 1]);
+                    const float b0 = __uint_as_float(rb[2 * l]), b1 = __uint_as_float(rb[2 * l + 1]);
+                    double      s  = (double) __fmul_rn(a0, a0);
+                    s += (double) __fmul_rn(a1, a1);
+                    s += (double) __fmul_rn(b0, b0);
+                    s += (double) __fmul_rn(b1, b1);
+                    t[l] = t[l] + s;  // butterfly level 16: lane l + lane l + 16
+                }
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) {
+#pragma unroll
+                    for (int l = 0; l < o; l++) {
+                        t[l] = t[l] + t[l + o];
+                    }
+                }
+                sc = rms_scale(t[0], 128, g.eps);
+            }
+#pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                uint32_t ra[32], rb[32];
+                tmem_ld32(tc0 + (uint32_t) (32 * c), ra);
+                tmem_ld32(tc0 + (uint32_t) (64 + 32 * c), rb);
+                float a[32], b[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    a[j] = __uint_as_float(ra[j]);
+                    b[j] = __uint_as_float(rb[j]);
+                    if (w) {
+                        a[j] = __fmul_rn(__fmul_rn(a[j], sc), __ldg(w + 32 * c + j));
+                        b[j] = __fmul_rn(__fmul_rn(b[j], sc), __ldg(w + 64 + 32 * c + j));
+                    }
+                }
+                if (g.rope && p >= 0) {
+                    const float * cr = g.rope + (int64_t) p * 128 + 64 * c;  // cos/sin of dims 32c ..
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float4 cs = __ldg(reinterpret_cast<const float4 *>(cr + 2 * j));
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            const float cv = e ? cs.z : cs.x, sv = e ? cs.w : cs.y;
+                            const float x0 = a[j + e], x1 = b[j + e];
+                            a[j + e]       = __fsub_rn(__fmul_rn(x0, cv), __fmul_rn(x1, sv));
+                            b[j + e]       = __fadd_rn(__fmul_rn(x0, sv), __fmul_rn(x1, cv));
+                        }
+                    }
+                }
+                if (p < 0) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        a[j] = 0.0f;
+                        b[j] = 0.0f;
+                    }
+                }
+                const int64_t col = (int64_t) hd * 128 + 32 * c;
+                put_rows32_f16<false>(sw, lane, a, g.qk, g.qk_ld, m_base, g.M, col);
+                put_rows32_f16<false>(sw, lane, b, g.qk, g.qk_ld, m_base, g.M, col + 64);
+                if (g.qk_lo) {
+                    put_rows32_f16<true>(sw, lane, a, g.qk + g.qk_lo, g.qk_ld, m_base, g.M, col);
+                    put_rows32_f16<true>(sw, lane, b, g.qk + g.qk_lo, g.qk_ld, m_base, g.M, col + 64);
+                }
+            }
+        } else {
+            const int     hv = hd - g.nq - g.nk;
+            const int64_t bb = m / g.seq, tt = m - bb * g.seq;
+            uint16_t *    dst = g.vt + ((bb * g.nk + hv) * 128) * g.vt_ld + tt;
+#pragma unroll 1
+            for (int c = 0; c < 4; c++) {
+                uint32_t r[32];
+                tmem_ld32(tc0 + (uint32_t) (32 * c), r);
+                if (m < g.M) {
+#pragma unroll 4
+                    for (int j = 0; j < 32; j++) {
+                        const float   x  = __uint_as_float(r[j]);
+                        const __half  hi = __float2half_rn(x);
+                        const int64_t o  = (int64_t) (32 * c + j) * g.vt_ld;
+                        dst[o]           = __half_as_ushort(hi);
+                        if (g.vt_lo) {
+                            dst[g.vt_lo + o] = __half_as_ushort(__float2half_rn(__fsub_rn(x, __half2float(hi))));
+                        }
+                    }
+                }
+            }
+        }
+    }
 }
 
 // ---- the kernel ------------------------------------------------------------------------------------
@@ -405,6 +586,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (g.swiglu) {
                 swiglu_epilogue(g, tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN), m_base,
                                 nt * 128, lane, stg);
+            } else if (g.qkv) {
+                qkv_epilogue(g, tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN), m_base, nt * kBN,
+                             lane, stg);
             } else {
             const int64_t n0     = nt * kBN;
             const bool    part   = g.splits > 1;  // raw partial of split w / tiles
@@ -820,6 +1004,103 @@ extern "C" acb_status acb_gemm_swiglu_quant(const void * A, int64_t lda, const v
         e = cudaLaunchKernelEx(&cfg, f16 ? gemm_tc_kernel<true, true> : gemm_tc_kernel<false, true>, ta, tb, g);
     } else {
         const int64_t work = ((M + 127) / 128) * (F / 128);
+        void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
+            f16 ? gemm_tc_kernel<true, false> : gemm_tc_kernel<false, false>;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) GemmCfg<false>::kSmem);
+        cfg.gridDim          = dim3((unsigned) (work < num_sms() ? work : num_sms()));
+        cfg.dynamicSmemBytes = GemmCfg<false>::kSmem;
+        e                    = cudaLaunchKernelEx(&cfg, kern, ta, tb, g);
+    }
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+extern "C" acb_status acb_gemm_qkv_planes(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M,
+                                          int64_t K, int n_q_heads, int n_kv_heads, const float * q_norm_w,
+                                          const float * k_norm_w, float eps, const int32_t * pos,
+                                          const float * rope_table, int max_pos, int64_t seq_len, uint16_t * qk,
+                                          int64_t qk_ld, int64_t qk_lo, uint16_t * vt, int64_t vt_ld, int64_t vt_lo,
+                                          int flags, int * err_flag, acb_stream_t stream) {
+    if (!A || !B || !qk || !vt || M <= 0 || K <= 0 || lda < K || ldb < K || n_q_heads <= 0 || n_kv_heads <= 0 ||
+        seq_len <= 0 || M % seq_len != 0 || qk_ld < (int64_t) (n_q_heads + n_kv_heads) * 128 || vt_ld < seq_len ||
+        qk_lo < 0 || vt_lo < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (rope_table && (!pos || max_pos <= 0)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (n_q_heads % 2 || n_kv_heads % 2 || K % kBK != 0 || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(A) % 16 != 0 || reinterpret_cast<uintptr_t>(B) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(qk) % 16 != 0 || qk_ld % 8 != 0 || qk_lo % 8 != 0 ||
+        reinterpret_cast<uintptr_t>(rope_table) % 16 != 0) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const int64_t N   = (int64_t) (n_q_heads + 2 * n_kv_heads) * 128;
+    GemmArgs      g   = {};
+    g.M               = M;
+    g.N               = N;
+    g.K               = K;
+    g.C               = qk;
+    g.c_type          = ACB_TYPE_F16;
+    g.ldc             = qk_ld;
+    g.rows_per_sample = 1;
+    g.err             = err_flag;
+    g.splits          = 1;
+    g.kps             = (int) (K / kBK);
+    g.qkv             = 1;
+    g.nq              = n_q_heads;
+    g.nk              = n_kv_heads;
+    g.qn              = q_norm_w;
+    g.kn              = k_norm_w;
+    g.eps             = eps;
+    g.pos             = pos;
+    g.rope            = rope_table;
+    g.max_pos         = max_pos;
+    g.seq             = seq_len;
+    g.qk              = qk;
+    g.qk_ld           = qk_ld;
+    g.qk_lo           = qk_lo;
+    g.vt              = vt;
+    g.vt_ld           = vt_ld;
+    g.vt_lo           = vt_lo;
+    const bool f16      = (flags & ACB_FLAG_F16) != 0;
+    const int  clusters = M > 128 ? pair_clusters(f16) : 0;
+    const bool pair     = clusters > 0;
+    CUtensorMap ta, tb;
+    if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, N, K, ldb, pair ? 128 : kBN, f16)) {
+        return ACB_ERR_CUDA;
+    }
+    g.group_m              = group_m_for(pair ? (M + 255) / 256 : (M + 127) / 128);
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim           = dim3(kGemmThreads);
+    cfg.stream             = (cudaStream_t) stream;
+    cudaLaunchAttribute attr[2];
+    int                 na = 0;
+    if (pair) {
+        attr[na].id               = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 2;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    if (flags & ACB_FLAG_PDL) {
+        attr[na].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    cfg.attrs    = na ? attr : nullptr;
+    cfg.numAttrs = na;
+    cudaError_t e;
+    if (pair) {
+        const int64_t work = ((M + 255) / 256) * (N / kBN);
+        cfg.gridDim          = dim3((unsigned) (2 * (work < clusters ? work : clusters)));
+        cfg.dynamicSmemBytes = GemmCfg<true>::kSmem;
+        e = cudaLaunchKernelEx(&cfg, f16 ? gemm_tc_kernel<true, true> : gemm_tc_kernel<false, true>, ta, tb, g);
+    } else {
+        const int64_t work = ((M + 127) / 128) * (N / kBN);
         void (*kern)(const CUtensorMap, const CUtensorMap, const GemmArgs) =
             f16 ? gemm_tc_kernel<true, false> : gemm_tc_kernel<false, false>;
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) GemmCfg<false>::kSmem);

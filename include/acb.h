@@ -250,6 +250,22 @@ ACB_API acb_status acb_gemm_swiglu_quant(const void * A, int64_t lda, const void
                                          void * Y, int y_type, int64_t ldy, int flags, int * err_flag,
                                          acb_stream_t stream);
 
+/* The fused q/k/v projection of an attention block with everything up to the attention operands
+ * in its epilogue: C = A . B^T with B = [Wq (n_q_heads*128 rows) | Wk | Wv (n_kv_heads*128 rows
+ * each)] stacked, then per q / k head RMSNorm (q_norm_w / k_norm_w, NULL: none) and, with a rope
+ * table, NeoX RoPE at pos[m] (ggml_rms_norm + ggml_mul + ggml_rope_ext of src/dit-graph.h:176-205,
+ * src/qwen3-enc.h:165-184), written as f16 into qk [M][qk_ld] (q heads then k heads; with qk_lo
+ * nonzero as exact hi / lo planes, lo qk_lo elements further); v heads go transposed into vt
+ * [(b*n_kv_heads + h)*128 + d][vt_ld] at column t for row m = b*seq_len + t (lo plane vt_lo
+ * further when nonzero). Bit-identical to acb_gemm_tc (f32 out) + acb_qk_norm_rope_planes +
+ * acb_attn_vt. Head counts even; rows with a position outside [0, max_pos) are written as
+ * zeros and flag ACB_DEVERR_POS_RANGE. */
+ACB_API acb_status acb_gemm_qkv_planes(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t K,
+                                       int n_q_heads, int n_kv_heads, const float * q_norm_w, const float * k_norm_w,
+                                       float eps, const int32_t * pos, const float * rope_table, int max_pos,
+                                       int64_t seq_len, uint16_t * qk, int64_t qk_ld, int64_t qk_lo, uint16_t * vt,
+                                       int64_t vt_ld, int64_t vt_lo, int flags, int * err_flag, acb_stream_t stream);
+
 ACB_API size_t     acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 
 /* Unsplit GEMMs with M > 128 run on CTA pairs (clusters of two, tcgen05 cta_group::2, 256 x 256

@@ -192,3 +192,34 @@ def test_gemm_swiglu_quant_matches_unfused(cuda, M, F, K, f16, vt, layout, bias)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("lo,rope", [(True, True), (False, True), (True, False)])
+def test_gemm_qkv_planes_matches_unfused(cuda, lo, rope):
+    """acb_gemm_qkv_planes (q/k RMSNorm + RoPE into attention operand planes and V^T planes in the
+    qkv GEMM's epilogue) == acb_gemm_tc (f32) + acb_qk_norm_rope_planes + acb_attn_vt, bit for bit.
+    300 tokens per sequence put sequence boundaries inside 32-row epilogue groups."""
+    import torch
+    Bs, S, nq, nk, K = 3, 300, 4, 2, 512
+    M = Bs * S
+    g = torch.Generator(device=cuda).manual_seed(31 + lo + 2 * rope)
+    A = torch.randn(M, K, device=cuda, generator=g).half()
+    B = (torch.randn((nq + 2 * nk) * 128, K, device=cuda, generator=g) * 0.05).half()
+    qw = 1 + 0.1 * torch.randn(128, device=cuda, generator=g)
+    kw = 1 + 0.1 * torch.randn(128, device=cuda, generator=g)
+    pos = torch.arange(S, dtype=torch.int32, device=cuda).repeat(Bs) if rope else None
+    tab = acb.rope_table(512, 128, 1e6).to(cuda) if rope else None
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    qk, vt, ld, vlo = acb.gemm_qkv_planes(A, B, nq, nk, qw, kw, 1e-6, S, pos=pos, rope=tab, lo=lo, err=err)
+    C = acb.gemm_bf16(A, B)
+    W = (nq + nk) * 128
+    want_qk = acb.qk_norm_rope_planes(C, nq, qw, 1e-6, pos=pos, rope=tab, n_k_heads=nk, k_w=kw)
+    want_vt, ld2, vlo2 = acb.attn_vt(C[:, W:].reshape(Bs, S, nk * 128), nk, lo=lo)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    if lo:
+        assert torch.equal(qk.view(torch.int16), want_qk.view(torch.int16))
+    else:
+        assert torch.equal(qk.view(torch.int16), want_qk[:M].view(torch.int16))
+    assert ld == ld2 and vlo == vlo2
+    assert torch.equal(vt.view(torch.int16), want_vt.view(torch.int16))
