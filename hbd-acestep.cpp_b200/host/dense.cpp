@@ -81,6 +81,19 @@ acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int
                        rows_per_sample, ACB_FLAG_PDL | L.op, s.ws, s.ws_bytes, s.err, (acb_stream_t) st);
 }
 
+acb_status dense_operand(const DenseLinear & L, bool exact, const float * x, int64_t xs, int M, const DenseScratch & s,
+                         cudaStream_t st, const NormSpec * norm, int64_t * width) {
+    const bool    three  = exact && L.split;
+    const int64_t Kp     = three ? 3 * (int64_t) L.K : L.K;
+    const int     layout = three ? ACB_LAYOUT_GEMM_A : ACB_LAYOUT_PLAIN;
+    *width               = Kp;
+    if (norm) {
+        return acb_norm_quant(x, xs, M, L.K, norm->w, norm->eps, norm->scale, norm->shift, norm->vec_stride,
+                              norm->rows_per_sample, L.vec, layout, s.xq, L.act_type(), Kp, 0, (acb_stream_t) st);
+    }
+    return acb_act_quant_ex(x, xs, 0, M, L.K, L.vec, layout, s.xq, L.act_type(), Kp, 0, (acb_stream_t) st);
+}
+
 bool dense_operand_spec(const DenseLinear & L, bool exact, int * o_type, int * flags, int64_t * width) {
     if (L.vec != ACB_TYPE_Q8_0 && L.vec != ACB_TYPE_F16 && L.vec != ACB_TYPE_BF16 && L.vec != ACB_TYPE_F32) {
         return false;

@@ -70,6 +70,11 @@ acb_status dense_forward(const DenseLinear & L, bool exact, const float * x, int
                          const float * gate, int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
                          cudaStream_t st, const NormSpec * norm = nullptr);
 
+// The activation operand of L for x (normalised first by `norm` when given) into s.xq, as
+// dense_forward produces it; *width = its row length (K, or 3K in the exact split layout).
+acb_status dense_operand(const DenseLinear & L, bool exact, const float * x, int64_t xs, int M, const DenseScratch & s,
+                         cudaStream_t st, const NormSpec * norm, int64_t * width);
+
 // How a fused producer (the attention epilogue, acb_attn_tc) writes L's activation operand into
 // s.xq itself: its o_type, flags (ACB_FLAG_GEMM_A for the exact layout) and row width. False when
 // only acb_act_quant_ex can produce it (Q8_K blocks span 256 columns).

@@ -288,7 +288,22 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ns_sa.scale           = scale_sa;
     ns_sa.shift           = shift_sa;
     ns_sa.rows_per_sample = R;
-    if (exact) {
+    if (Nh % 2 == 0 && Nkv % 2 == 0) {
+        // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue: the hi (and,
+        // exact, lo) planes of Q||K and of V^T for the tensor-core attention
+        const int64_t W  = QD + KD;
+        const int64_t lo = exact ? (int64_t) R * W : 0;
+        uint16_t *    hi = planes.as<uint16_t>();
+        const int64_t vl = exact ? (int64_t) Ng * KD * s_ld : 0;
+        int64_t       Kp = 0;
+        ACB_TRY(dense_operand(L.sa_qkv, exact, hp, H, R, sc, s, &ns_sa, &Kp));
+        ACB_TRY(acb_gemm_qkv_planes(sc.xq, Kp, L.sa_qkv.w, L.sa_qkv.ldw, R, Kp, Nh, Nkv,
+                                    (const float *) L.sa_q_norm->data, (const float *) L.sa_k_norm->data, eps,
+                                    pos.as<int32_t>(), rope.as<float>(), S, S, hi, W, lo, vtb.as<uint16_t>(), s_ld, vl,
+                                    kPdl | L.sa_qkv.op, e, as));
+        ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
+                            c.sliding_window, 0, scale, kPdl | ao_flags, lo, lo, vl, e, as));
+    } else if (exact) {
         float * q32 = qkv32.as<float>();
         ACB_TRY(dense_forward(L.sa_qkv, true, hp, H, 0, R, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0, 0,
                               sc, s, &ns_sa));

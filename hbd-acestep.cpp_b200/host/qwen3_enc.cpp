@@ -175,7 +175,20 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
         NormSpec ns_in;
         ns_in.w   = (const float *) L.attn_norm->data;
         ns_in.eps = eps;
-        if (exact) {
+        if (Nh % 2 == 0 && Nkv % 2 == 0) {
+            // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue
+            const int64_t W  = QD + KD;
+            const int64_t lo = exact ? (int64_t) cap * W : 0;
+            const int64_t vl = exact ? (int64_t) KD * s_ld : 0;
+            uint16_t *    hi = planes.as<uint16_t>();
+            int64_t       Kp = 0;
+            ACB_TRY(dense_operand(L.qkv, exact, hp, H, S, sc, s, &ns_in, &Kp));
+            ACB_TRY(acb_gemm_qkv_planes(sc.xq, Kp, L.qkv.w, L.qkv.ldw, S, Kp, Nh, Nkv, (const float *) L.q_norm->data,
+                                        (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap,
+                                        S, hi, W, lo, vtb.as<uint16_t>(), s_ld, vl, kPdl | L.qkv.op, e, as));
+            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+                                scale, kPdl | ao_flags, lo, lo, vl, e, as));
+        } else if (exact) {
             float * q32 = qkv32.as<float>();
             ACB_TRY(dense_forward(L.qkv, true, hp, H, 0, S, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0,
                                   0, sc, s, &ns_in));
