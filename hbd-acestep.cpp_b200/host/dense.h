@@ -86,6 +86,10 @@ acb_status dense_forward_operand(const DenseLinear & L, bool exact, int M, void 
                                  int64_t gate_stride, int64_t rows_per_sample, const DenseScratch & s,
                                  cudaStream_t st);
 
+// Rows from which the q/k/v projection runs with the QKV epilogue (acb_gemm_qkv_planes; fewer rows
+// take the split-K GEMM and the separate norm / transpose passes).
+constexpr int kQkvFuseMinRows = 1024;
+
 // Rows from which the feed-forward block runs its gate/up GEMM with the SwiGLU epilogue (the
 // fused form needs whole waves of 256-row tiles to pay off; fewer rows take the split-K path).
 constexpr int kFfnFuseMinRows = 1024;

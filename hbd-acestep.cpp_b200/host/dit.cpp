@@ -288,7 +288,7 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ns_sa.scale           = scale_sa;
     ns_sa.shift           = shift_sa;
     ns_sa.rows_per_sample = R;
-    if (Nh % 2 == 0 && Nkv % 2 == 0) {
+    if (Nh % 2 == 0 && Nkv % 2 == 0 && R >= kQkvFuseMinRows) {
         // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue: the hi (and,
         // exact, lo) planes of Q||K and of V^T for the tensor-core attention
         const int64_t W  = QD + KD;

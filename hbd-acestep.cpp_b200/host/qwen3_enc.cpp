@@ -175,7 +175,7 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
         NormSpec ns_in;
         ns_in.w   = (const float *) L.attn_norm->data;
         ns_in.eps = eps;
-        if (Nh % 2 == 0 && Nkv % 2 == 0) {
+        if (Nh % 2 == 0 && Nkv % 2 == 0 && S >= kQkvFuseMinRows) {
             // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue
             const int64_t W  = QD + KD;
             const int64_t lo = exact ? (int64_t) cap * W : 0;
