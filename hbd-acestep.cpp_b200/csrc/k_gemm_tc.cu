@@ -1024,9 +1024,9 @@ extern "C" acb_status acb_gemm_qkv_planes(const void * A, int64_t lda, const voi
                                           const float * rope_table, int max_pos, int64_t seq_len, uint16_t * qk,
                                           int64_t qk_ld, int64_t qk_lo, uint16_t * vt, int64_t vt_ld, int64_t vt_lo,
                                           int flags, int * err_flag, acb_stream_t stream) {
-    if (!A || !B || !qk || !vt || M <= 0 || K <= 0 || lda < K || ldb < K || n_q_heads <= 0 || n_kv_heads <= 0 ||
-        seq_len <= 0 || M % seq_len != 0 || qk_ld < (int64_t) (n_q_heads + n_kv_heads) * 128 || vt_ld < seq_len ||
-        qk_lo < 0 || vt_lo < 0) {
+    if (!A || !B || !qk || (n_kv_heads > 0 && !vt) || M <= 0 || K <= 0 || lda < K || ldb < K || n_q_heads <= 0 ||
+        n_kv_heads < 0 || seq_len <= 0 || M % seq_len != 0 || qk_ld < (int64_t) (n_q_heads + n_kv_heads) * 128 ||
+        (n_kv_heads > 0 && vt_ld < seq_len) || qk_lo < 0 || vt_lo < 0) {
         return ACB_ERR_INVALID_ARG;
     }
     if (rope_table && (!pos || max_pos <= 0)) {

@@ -344,9 +344,20 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     NormSpec ns_ca;
     ns_ca.w   = (const float *) L.ca_norm->data;
     ns_ca.eps = eps;
-    float * cq = qkv32.as<float>();
-    ACB_TRY(dense_forward(L.ca_q, exact, hp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc, s,
-                          &ns_ca));
+    // the query's RMSNorm (q_norm) into the attention operand planes: in the q projection's epilogue
+    // (from 1024 rows), else through f32
+    const bool cq_fused = Nh % 2 == 0 && R >= kQkvFuseMinRows;
+    float *    cq       = qkv32.as<float>();
+    if (cq_fused) {
+        int64_t Kp = 0;
+        ACB_TRY(dense_operand(L.ca_q, exact, hp, H, R, sc, s, &ns_ca, &Kp));
+        ACB_TRY(acb_gemm_qkv_planes(sc.xq, Kp, L.ca_q.w, L.ca_q.ldw, R, Kp, Nh, 0, (const float *) L.ca_q_norm->data,
+                                    nullptr, eps, nullptr, nullptr, 0, R, planes.as<uint16_t>(), QD,
+                                    exact ? (int64_t) R * QD : 0, nullptr, 0, 0, kPdl | L.ca_q.op, e, as));
+    } else {
+        ACB_TRY(dense_forward(L.ca_q, exact, hp, H, 0, R, cq, ACB_TYPE_F32, QD, nullptr, nullptr, 0, nullptr, 0, 0, sc,
+                              s, &ns_ca));
+    }
     int     co_type = ACB_TYPE_F32, co_flags = 0;
     int64_t co_ts   = QD;
     void *  co      = att.p;
@@ -363,14 +374,19 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     if (exact) {
         const int64_t lo = (int64_t) R * QD;
         uint16_t *    qh = planes.as<uint16_t>();
-        ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, (const float *) L.ca_q_norm->data, 0,
-                                        nullptr, D, eps, nullptr, nullptr, 0, e, as));
+        if (!cq_fused) {
+            ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, (const float *) L.ca_q_norm->data,
+                                            0, nullptr, D, eps, nullptr, nullptr, 0, e, as));
+        }
         ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
                             0, scale, kPdl | co_flags, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
     } else {
-        ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
-                                 (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
-        ACB_TRY(acb_attn_tc(q16.p, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0,
+        uint16_t * q16p = cq_fused ? planes.as<uint16_t>() : q16.as<uint16_t>();
+        if (!cq_fused) {
+            ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
+                                     (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
+        }
+        ACB_TRY(acb_attn_tc(q16p, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0,
                             0, 0, scale, kPdl | co_flags, 0, 0, 0, e, as));
     }
     if (fuse_co) {

@@ -258,8 +258,9 @@ ACB_API acb_status acb_gemm_swiglu_quant(const void * A, int64_t lda, const void
  * nonzero as exact hi / lo planes, lo qk_lo elements further); v heads go transposed into vt
  * [(b*n_kv_heads + h)*128 + d][vt_ld] at column t for row m = b*seq_len + t (lo plane vt_lo
  * further when nonzero). Bit-identical to acb_gemm_tc (f32 out) + acb_qk_norm_rope_planes +
- * acb_attn_vt. Head counts even; rows with a position outside [0, max_pos) are written as
- * zeros and flag ACB_DEVERR_POS_RANGE. */
+ * acb_attn_vt. Head counts even; n_kv_heads 0 is the q projection alone (vt unused: the
+ * cross-attention query of src/dit-graph.h:300-316). Rows with a position outside [0, max_pos)
+ * are written as zeros and flag ACB_DEVERR_POS_RANGE. */
 ACB_API acb_status acb_gemm_qkv_planes(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t K,
                                        int n_q_heads, int n_kv_heads, const float * q_norm_w, const float * k_norm_w,
                                        float eps, const int32_t * pos, const float * rope_table, int max_pos,
