@@ -70,6 +70,7 @@ def lib():
             "acb_attn_prefill": (I, [P, I64, I64, P, I64, I64, P, I64, I64, P, I, I64, I64, I, I, I, I, I, I, I, I,
                                      I, F, I, P]),
             "acb_gemv": (I, [P, I, I64, I64, I, I, P, I64, P, F, I, P, I64, I, P, I64, I, P, P]),
+            "acb_q8_0_to_tiles": (I, [P, P, I64, I64, P]),
             "acb_qkv_post": (I, [P, I64, I64, I, I, I, P, P, F, P, P, I, P, I64, P, P, I, I, I, I, P, P]),
             "acb_attn_decode_splits": (I, [I, I]),
             "acb_attn_decode": (I, [P, I64, I, I, I, I, P, P, P, I, I, I, F, I, P, P, P, P, I64, P, I, P]),
@@ -257,6 +258,17 @@ EPI_STORE, EPI_ADD = 0, 1
 FLAG_PDL = 1
 FLAG_F16 = 2  # tensor-core operands are f16 (acb_gemm_bf16, acb_attn_prefill)
 FLAG_GEMM_A = 4  # acb_attn_tc: quantised output in the exact [hi | hi | lo] operand layout
+
+
+Q8_0_TILES = 1008
+
+
+def q8_0_to_tiles(W, N, K, stream=None):
+    """GGUF Q8_0 rows (uint8 tensor) -> the tensor-core GEMV's tiled copy (w_type Q8_0_TILES)."""
+    import torch
+    out = torch.empty_like(W)
+    _check("acb_q8_0_to_tiles", lib().acb_q8_0_to_tiles(_ptr(W), _ptr(out), N, K, _stream(stream)))
+    return out
 
 
 def gemv(W, w_type, N, K, x, M=None, prologue=PRO_X, x_stride=None, norm_w=None, eps=1e-6, n_split=1, y=None,

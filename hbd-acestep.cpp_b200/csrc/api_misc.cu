@@ -57,6 +57,7 @@ extern "C" int64_t acb_row_bytes(int type, int64_t n) {
             be = 1, bb = 2;
             break;
         case ACB_TYPE_Q8_0:
+        case ACB_TYPE_Q8_0_TILES:
             be = 32, bb = 34;
             break;
         case ACB_TYPE_Q4_K:

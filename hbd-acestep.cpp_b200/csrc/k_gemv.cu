@@ -586,6 +586,260 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
     }
 }
 
+// ---- Q8_0 repacked into 16-row MMA tiles (ACB_TYPE_Q8_0_TILES) ------------------------------
+// Tile t (rows 16t .. 16t+15), K-block b (32 columns) is 544 bytes: 512 bytes of int8 weights in
+// the order of the A operand of mma.m16n8k32 (lane l = 4g + q holds rows g and g+8, columns
+// 4q..4q+3 and 16+4q..16+4q+3, 16 bytes) followed by eight words (d[16t+g] | d[16t+g+8] << 16) of
+// f16 block scales. Tiles are stored tile-major, blocks in K order: the same bytes as Q8_0 rows.
+constexpr int kTileBytes = 544;
+
+__device__ __forceinline__ void mma_s8_16832(const uint4 & a, int b0, int b1, int * c) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+
+// One warp per (tile, 544-byte block): repack from GGUF Q8_0 rows.
+__global__ void __launch_bounds__(256) q8_0_to_tiles_kernel(const uint8_t * __restrict__ src, uint8_t * __restrict__ dst,
+                                                            int64_t n_tiles, int nb) {
+    const int     lane = threadIdx.x & 31;
+    const int64_t item = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (item >= n_tiles * nb) {
+        return;
+    }
+    const int64_t t = item / nb;
+    const int     b = (int) (item - t * nb);
+    const int     g = lane >> 2, q = lane & 3;
+    const int64_t rb = (int64_t) nb * 34;
+    auto          qs = [&](int r, int k) -> uint32_t {  // 4 int8 of row r at columns k..k+3 of block b
+        const uint8_t * blk = src + (16 * t + r) * rb + (int64_t) b * 34 + 2;
+        return (uint32_t) blk[k] | ((uint32_t) blk[k + 1] << 8) | ((uint32_t) blk[k + 2] << 16) |
+               ((uint32_t) blk[k + 3] << 24);
+    };
+    uint8_t * o = dst + item * kTileBytes;
+    reinterpret_cast<uint4 *>(o)[lane] = make_uint4(qs(g, 4 * q), qs(g + 8, 4 * q), qs(g, 16 + 4 * q), qs(g + 8, 16 + 4 * q));
+    if (lane < 8) {
+        const uint8_t * d0 = src + (16 * t + lane) * rb + (int64_t) b * 34;
+        const uint8_t * d1 = src + (16 * t + lane + 8) * rb + (int64_t) b * 34;
+        reinterpret_cast<uint32_t *>(o + 512)[lane] = (uint32_t) d0[0] | ((uint32_t) d0[1] << 8) |
+                                                      ((uint32_t) d1[0] << 16) | ((uint32_t) d1[1] << 24);
+    }
+}
+
+// Tensor-core GEMV over tiled Q8_0 weights: each CTA streams a contiguous range of tiles through
+// the shared-memory ring in stages of bs K-blocks (whole tiles when K <= 2048); warp w takes
+// blocks w, w+16, ... of a stage and issues one mma.m16n8k32 (int8, int32 sums exact) per block,
+// scaling each block's sums by d_w * d_x and adding them in fp32 (ggml's vec_dot_q8_0_q8_0
+// arithmetic per block); at the end of a tile the 16 warps' partials are added in warp order.
+template <int MT, int PRO>
+__global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParams p, int bs) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t * full  = reinterpret_cast<uint64_t *>(smem);
+    uint64_t * empty = full + 8;
+    double *   red   = reinterpret_cast<double *>(smem + 128);
+    int8_t *   xq    = reinterpret_cast<int8_t *>(smem + kHdr);
+    const int  nb       = p.K / 32;
+    const int  xq_bytes = (MT * p.K + 15) / 16 * 16;
+    float *    xd       = reinterpret_cast<float *>(smem + kHdr + xq_bytes);
+    const int  xd_bytes = (MT * nb * 4 + 15) / 16 * 16;
+    float *    tred     = reinterpret_cast<float *>(smem + kHdr + xq_bytes + xd_bytes);  // [16 warps][32][4]
+    const int  st_off   = (kHdr + xq_bytes + xd_bytes + kConsumerWarps * 32 * 4 * 4 + 127) / 128 * 128;
+    uint8_t *  stages   = smem + st_off;
+
+    const int64_t n_tiles = p.N / 16;
+    const int64_t t0      = (int64_t) blockIdx.x * p.rows_per_cta;  // rows_per_cta holds tiles per CTA here
+    const int64_t t1      = t0 + p.rows_per_cta < n_tiles ? t0 + p.rows_per_cta : n_tiles;
+    const int     parts   = nb / bs;
+    const int     nstage  = t1 > t0 ? (int) ((t1 - t0) * parts) : 0;
+    const int     sbytes  = bs * kTileBytes;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < p.stages; s++) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], kConsumerWarps);
+        }
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    ptx::grid_dep_launch();
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            const uint64_t pol = ptx::policy_evict_first();
+            const uint8_t * src = p.W + t0 * (int64_t) nb * kTileBytes;
+            for (int i = 0; i < nstage; i++) {
+                const int s = i % p.stages;
+                if (i >= p.stages && !ptx::mbar_wait(&empty[s], ((i / p.stages) - 1) & 1)) {
+                    if (p.err) {
+                        atomicOr(p.err, ACB_DEVERR_TIMEOUT);
+                    }
+                    break;
+                }
+                ptx::mbar_arrive_expect_tx(&full[s], (uint32_t) sbytes);
+                ptx::bulk_g2s_stream(stages + (int64_t) s * p.stage_bytes, src + (int64_t) i * sbytes,
+                                     (uint32_t) sbytes, &full[s], pol);
+            }
+        }
+        return;
+    }
+
+    ptx::grid_dep_wait();
+    quantize_q8_0<PRO>(p, xq, xd, red);
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+
+    const int g = lane >> 2, q = lane & 3;
+    // this lane's batch column of the B operand (n = g) and of the accumulators (n = 2q, 2q + 1)
+    const int8_t * xb  = xq + (int64_t) (g < MT ? g : 0) * p.K;
+    const bool     bok = g < p.M;
+    float          acc[4] = { 0.0f, 0.0f, 0.0f, 0.0f };  // (row g, n 2q), (g, 2q+1), (g+8, 2q), (g+8, 2q+1)
+    for (int i = 0; i < nstage; i++) {
+        const int s = i % p.stages;
+        if (!ptx::mbar_wait(&full[s], (i / p.stages) & 1)) {
+            if (lane == 0 && p.err) {
+                atomicOr(p.err, ACB_DEVERR_TIMEOUT);
+            }
+            return;
+        }
+        const int       part  = i % parts;
+        const uint8_t * stage = stages + (int64_t) s * p.stage_bytes;
+        for (int bl = warp; bl < bs; bl += kConsumerWarps) {
+            const int     b  = part * bs + bl;
+            const uint4   a  = *reinterpret_cast<const uint4 *>(stage + bl * kTileBytes + lane * 16);
+            const uint32_t dw = *reinterpret_cast<const uint32_t *>(stage + bl * kTileBytes + 512 + g * 4);
+            const int     b0 = bok ? *reinterpret_cast<const int *>(xb + 32 * b + 4 * q) : 0;
+            const int     b1 = bok ? *reinterpret_cast<const int *>(xb + 32 * b + 16 + 4 * q) : 0;
+            int           c[4];
+            mma_s8_16832(a, b0, b1, c);
+            const float dr[2] = { f16_bits_to_f((uint16_t) (dw & 0xffff)), f16_bits_to_f((uint16_t) (dw >> 16)) };
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int n = 2 * q + j;
+                if (n < p.M) {
+                    const float dx = xd[n * nb + b];
+#pragma unroll
+                    for (int r = 0; r < 2; r++) {
+                        acc[2 * r + j] = __fadd_rn(acc[2 * r + j], __fmul_rn((float) c[2 * r + j], __fmul_rn(dr[r], dx)));
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            ptx::mbar_arrive(&empty[s]);
+        }
+        if (part == parts - 1) {
+            // tile complete: add the 16 warps' partials in warp order and store
+            *reinterpret_cast<float4 *>(tred + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+            if (warp == 0) {
+                float v[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+                for (int w = 0; w < kConsumerWarps; w++) {
+                    const float4 t = *reinterpret_cast<const float4 *>(tred + (w * 32 + lane) * 4);
+                    v[0]           = __fadd_rn(v[0], t.x);
+                    v[1]           = __fadd_rn(v[1], t.y);
+                    v[2]           = __fadd_rn(v[2], t.z);
+                    v[3]           = __fadd_rn(v[3], t.w);
+                }
+                const int64_t tile = t0 + i / parts;
+#pragma unroll
+                for (int r = 0; r < 2; r++) {
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const int n = 2 * q + j;
+                        if (n < p.M) {
+                            const int64_t row = tile * 16 + g + 8 * r;
+                            float *       yp  = p.y + (int64_t) n * p.y_stride + row;
+                            const float   val = v[2 * r + j];
+                            *yp = p.epilogue == EPI_ADD ? __fadd_rn(p.res[(int64_t) n * p.res_stride + row], val) : val;
+                        }
+                    }
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+        }
+    }
+}
+
+template <int MT, int PRO>
+static acb_status launch_gemv_tiles(GemvParams p, bool pdl, cudaStream_t st) {
+    const int     sms     = num_sms();
+    const int     nb      = p.K / 32;
+    const int64_t n_tiles = p.N / 16;
+    // K-blocks per stage: the largest divisor of nb up to 64 (whole tiles for K <= 2048)
+    int bs = 1;
+    for (int d = 1; d <= 64 && d <= nb; d++) {
+        if (nb % d == 0) {
+            bs = d;
+        }
+    }
+    const int64_t per_cta = (n_tiles + sms - 1) / sms;
+    const int     grid    = (int) ((n_tiles + per_cta - 1) / per_cta);
+    p.rows_per_cta        = (int) per_cta;  // tiles per CTA
+    p.stage_bytes         = bs * kTileBytes;
+    const int xq_bytes = (MT * p.K + 15) / 16 * 16;
+    const int xd_bytes = (MT * nb * 4 + 15) / 16 * 16;
+    const int st_off   = (kHdr + xq_bytes + xd_bytes + kConsumerWarps * 32 * 4 * 4 + 127) / 128 * 128;
+    const int64_t nstage = per_cta * (nb / bs);
+    int           stages = nstage < 6 ? (int) nstage : 6;
+    const int64_t smem_cap = nstage > 4 ? 200 * 1024 : 110 * 1024;
+    while (stages > 1 && st_off + (int64_t) stages * p.stage_bytes > smem_cap) {
+        stages--;
+    }
+    p.stages = stages < 1 ? 1 : stages;
+    const int64_t smem = st_off + (int64_t) p.stages * p.stage_bytes;
+    if (smem > 220 * 1024) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    auto kern = gemv_tiles_kernel<MT, PRO>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) grid);
+    cfg.blockDim           = dim3(kThreads);
+    cfg.dynamicSmemBytes   = (size_t) smem;
+    cfg.stream             = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = pdl ? attr : nullptr;
+    cfg.numAttrs                                       = pdl ? 1 : 0;
+    cudaError_t e                                      = cudaLaunchKernelEx(&cfg, kern, p, bs);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+template <int PRO>
+static acb_status dispatch_tiles_mp(const GemvParams & p, bool pdl, cudaStream_t st) {
+    if (p.M <= 1) {
+        return launch_gemv_tiles<1, PRO>(p, pdl, st);
+    }
+    if (p.M <= 2) {
+        return launch_gemv_tiles<2, PRO>(p, pdl, st);
+    }
+    if (p.M <= 4) {
+        return launch_gemv_tiles<4, PRO>(p, pdl, st);
+    }
+    return launch_gemv_tiles<8, PRO>(p, pdl, st);
+}
+
+static acb_status dispatch_tiles(const GemvParams & p, bool pdl, cudaStream_t st) {
+    switch (p.prologue) {
+        case PRO_RMSNORM:
+            return dispatch_tiles_mp<PRO_RMSNORM>(p, pdl, st);
+        case PRO_SUM_SPLITS:
+            return dispatch_tiles_mp<PRO_SUM_SPLITS>(p, pdl, st);
+        case PRO_SWIGLU:
+            return dispatch_tiles_mp<PRO_SWIGLU>(p, pdl, st);
+        default:
+            return dispatch_tiles_mp<PRO_X>(p, pdl, st);
+    }
+}
+
 template <int QT, int MT, int PRO>
 static acb_status launch_gemv(GemvParams p, bool pdl, cudaStream_t st) {
     const int sms = num_sms();
@@ -720,6 +974,12 @@ extern "C" acb_status acb_gemv(const void * W, int w_type, int64_t N, int64_t K,
             }
             p.row_bytes = K / 32 * 34;
             return dispatch_m<ACB_TYPE_Q8_0>(p, pdl, st);
+        case ACB_TYPE_Q8_0_TILES:
+            if (K % 256 != 0 || N % 16 != 0) {
+                return ACB_ERR_UNSUPPORTED;
+            }
+            p.row_bytes = K / 32 * 34;
+            return dispatch_tiles(p, pdl, st);
         case ACB_TYPE_Q4_K:
             if (K % 256 != 0) {
                 return ACB_ERR_UNSUPPORTED;
@@ -735,4 +995,17 @@ extern "C" acb_status acb_gemv(const void * W, int w_type, int64_t N, int64_t K,
         default:
             return ACB_ERR_UNSUPPORTED;
     }
+}
+
+extern "C" acb_status acb_q8_0_to_tiles(const void * src, void * dst, int64_t N, int64_t K, acb_stream_t stream) {
+    if (!src || !dst || N <= 0 || K <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (N % 16 != 0 || K % 32 != 0 || reinterpret_cast<uintptr_t>(dst) % 16 != 0) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const int64_t items = (N / 16) * (K / 32);
+    q8_0_to_tiles_kernel<<<(unsigned) ((items + 7) / 8), 256, 0, (cudaStream_t) stream>>>(
+        reinterpret_cast<const uint8_t *>(src), reinterpret_cast<uint8_t *>(dst), N / 16, (int) (K / 32));
+    return launch_status();
 }

@@ -51,6 +51,8 @@ struct acb_qw3lm {
     std::vector<LMLayer> layers;
     DevBuf               head2;
     DevTensor            head2_t;
+    DevBuf               head_tiles;  // the LM head (tied embedding) repacked for the tensor-core GEMV
+    DevTensor            head_tiles_t;
     int                  head2_off = -1;
     int                  n_sets    = 1;
     std::vector<int>     kv_pos;
@@ -179,7 +181,7 @@ const DevTensor * head_for(acb_qw3lm * m, int lm_offset, int lm_count, int * out
         return &m->head2_t;
     }
     *out_v = m->c.vocab_size;
-    return m->embed;
+    return m->head_tiles_t.valid() ? &m->head_tiles_t : m->embed;
 }
 
 // step graph: [embed gather] [layers] [head] (+ argmax/advance when greedy)
@@ -334,6 +336,52 @@ extern "C" acb_status acb_qw3lm_load(const char * gguf_path, int max_seq_len, in
             return bad(s, A.error);
         }
     }
+    {
+        // Q8_0 linears (N a multiple of 16) repacked in place into the tensor-core GEMV's tiles;
+        // the embedding keeps its GGUF rows for get_rows and gets a tiled copy for the head
+        size_t big = 0;
+        auto   tileable = [](const DevTensor * t) { return t && t->type == ACB_TYPE_Q8_0 && t->N % 16 == 0; };
+        std::vector<DevTensor *> lin;
+        for (LMLayer & L : m->layers) {
+            for (DevTensor * t : { L.qkv, L.qk, L.q, L.k, L.v, L.o, L.gate_up, L.gate, L.up, L.down }) {
+                if (tileable(t)) {
+                    lin.push_back(t);
+                    big = std::max(big, (size_t) t->N * (size_t) t->row_bytes());
+                }
+            }
+        }
+        DevBuf tmp;
+        if (!lin.empty() && tmp.alloc(big, false) != ACB_OK) {
+            return bad(ACB_ERR_OOM, "repack buffer allocation failed");
+        }
+        for (DevTensor * t : lin) {
+            const size_t bytes = (size_t) t->N * (size_t) t->row_bytes();
+            if (cudaMemcpyAsync(tmp.p, t->data, bytes, cudaMemcpyDeviceToDevice, m->st) != cudaSuccess) {
+                return bad(ACB_ERR_CUDA, "repack copy failed");
+            }
+            acb_status s = acb_q8_0_to_tiles(tmp.p, t->data, t->N, t->K, (acb_stream_t) m->st);
+            if (s != ACB_OK) {
+                return bad(s, "repack failed");
+            }
+            t->type = ACB_TYPE_Q8_0_TILES;
+        }
+        if (tileable(m->embed) && m->embed->N >= c.vocab_size) {
+            const int64_t n = (int64_t) c.vocab_size / 16 * 16;
+            if (n == c.vocab_size && m->head_tiles.alloc((size_t) n * m->embed->row_bytes(), false) == ACB_OK) {
+                acb_status s = acb_q8_0_to_tiles(m->embed->data, m->head_tiles.p, n, m->embed->K, (acb_stream_t) m->st);
+                if (s != ACB_OK) {
+                    return bad(s, "head repack failed");
+                }
+                m->head_tiles_t      = *m->embed;
+                m->head_tiles_t.type = ACB_TYPE_Q8_0_TILES;
+                m->head_tiles_t.data = m->head_tiles.p;
+                m->head_tiles_t.N    = n;
+            }
+        }
+        if (cudaStreamSynchronize(m->st) != cudaSuccess) {
+            return bad(ACB_ERR_CUDA, "repack failed");
+        }
+    }
 
     // KV cache [L][n_sets][Nkv][max_seq][D] f16, zeroed (qw3lm_alloc_kv_cache, qwen3-lm.h:173-224)
     const int D = c.head_dim, S = c.max_seq_len;
@@ -476,7 +524,7 @@ extern "C" acb_status acb_qw3lm_forward(acb_qw3lm * m, const int32_t * token_ids
                              m->hidden.p, ACB_TYPE_F32, H, m->err.as<int>(), (acb_stream_t) m->st));
         ACB_TRY(enqueue_layers(m, n, kv_set, 0));
         if (c0 + n == n_tokens && logits) {
-            ACB_TRY(gemv_rows(m, m->embed, 0, c.vocab_size, 1, ACB_PRO_RMSNORM, m->hidden.as<float>() + (size_t) (n - 1) * H,
+            ACB_TRY(gemv_rows(m, m->head_tiles_t.valid() ? &m->head_tiles_t : m->embed, 0, c.vocab_size, 1, ACB_PRO_RMSNORM, m->hidden.as<float>() + (size_t) (n - 1) * H,
                               H, (const float *) m->final_norm->data, 0, m->logits.as<float>(), c.vocab_size,
                               ACB_EPI_STORE, nullptr, 0));
             cudaMemcpyAsync(logits, m->logits.p, sizeof(float) * c.vocab_size, cudaMemcpyDeviceToHost, m->st);

@@ -58,6 +58,8 @@ typedef enum {
     ACB_TYPE_Q8_K = 15,
     ACB_TYPE_I32  = 26,
     ACB_TYPE_BF16 = 30,
+    /* not a GGUF type: Q8_0 weights repacked by acb_q8_0_to_tiles for the tensor-core GEMV */
+    ACB_TYPE_Q8_0_TILES = 1008,
 } acb_type;
 
 enum {
@@ -380,6 +382,11 @@ enum {
  * add. Replaces ggml_mul_mat at every decode linear (src/qwen3-lm.h:639-651, 747-755) together
  * with the ggml_rms_norm/ggml_mul before it (qwen3-lm.h:636,741), ggml_swiglu
  * (qwen3-enc.h:217) and ggml_add after it (qwen3-lm.h:730,738). */
+/* Repack GGUF Q8_0 rows [N][K] (N a multiple of 16) into 16-row tiles for acb_gemv with w_type
+ * ACB_TYPE_Q8_0_TILES: per tile and 32-column block, 512 bytes of int8 weights in the order of the
+ * A operand of an int8 mma.m16n8k32 followed by the 16 rows' f16 scales -- the same byte count as
+ * the GGUF rows, and the same values. No reference counterpart (an on-device layout). */
+ACB_API acb_status acb_q8_0_to_tiles(const void * src, void * dst, int64_t N, int64_t K, acb_stream_t stream);
 ACB_API acb_status acb_gemv(const void * W, int w_type, int64_t N, int64_t K, int M, int prologue, const float * x,
                             int64_t x_stride, const float * norm_w, float eps, int n_split, float * y,
                             int64_t y_stride, int epilogue, const float * res, int64_t res_stride, int flags,

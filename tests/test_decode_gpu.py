@@ -256,3 +256,27 @@ def test_lm_errors(cuda, tmp_path):
         gpu.forward(np.zeros(300, np.int32))  # exceeds max_seq 256
     assert e.value.status == 4
     gpu.close()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 2048), (1, 2048, 6144), (3, 512, 2048), (8, 256, 9728), (1, 1024, 2560)])
+def test_gemv_q8_0_tiles(cuda, M, N, K):
+    """Q8_0 weights repacked into tensor-core tiles (acb_q8_0_to_tiles, w_type Q8_0_TILES): the
+    int8 mma path against the oracle's quantised mul_mat (same per-block integer sums and
+    scales; only the fp32 order of the block sums differs), with every prologue and the
+    residual epilogue."""
+    rng = np.random.default_rng(N + K + M)
+    W = O.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32), O.Q8_0)
+    Wt = acb.q8_0_to_tiles(TW(W, cuda), N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    y = acb.gemv(Wt, acb.Q8_0_TILES, N, K, T(x, cuda), M=M)
+    assert max_rel(y.cpu().numpy(), O.mul_mat(O.Q8_0, W, N, K, x)) <= 2e-6
+    w = (1 + 0.01 * rng.standard_normal(K)).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    y = acb.gemv(Wt, acb.Q8_0_TILES, N, K, T(x * 3, cuda), M=M, prologue=acb.PRO_RMSNORM, norm_w=T(w, cuda),
+                 epilogue=acb.EPI_ADD, res=T(res, cuda), flags=acb.FLAG_PDL)
+    ref = res + O.mul_mat(O.Q8_0, W, N, K, O.rms_norm(x * 3, w, 1e-6))
+    assert max_rel(y.cpu().numpy() - res, ref - res) <= 2e-6
+    gu = rng.standard_normal((M, 2 * K)).astype(np.float32)
+    y = acb.gemv(Wt, acb.Q8_0_TILES, N, K, T(gu, cuda), M=M, prologue=acb.PRO_SWIGLU, x_stride=2 * K)
+    ref = O.mul_mat(O.Q8_0, W, N, K, O.swiglu(gu[:, :K], gu[:, K:]))
+    assert max_rel(y.cpu().numpy(), ref) <= 5e-4 and cos_sim(y.cpu().numpy(), ref) > 0.999999
