@@ -525,18 +525,24 @@ def run_gemv_shapes(dev, reps=20):
         W[: N * rb].view(N, K // 32, 34)[:, :, 0:2] = torch.tensor([0x00, 0x14], dtype=torch.uint8, device=dev)
         x = torch.randn(1, K, device=dev)
         y = torch.empty(1, N, device=dev)
-        for _ in range(3):
-            acb.gemv(W, acb.Q8_0, N, K, x, y=y)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            acb.gemv(W, acb.Q8_0, N, K, x, y=y)
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) / reps * 1e3
         nbytes = N * rb + K * 4 + N * 4
-        out["shapes"][name] = {"N": N, "K": K, "us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1)}
-        del W
+        res = {"N": N, "K": K}
+        Wt = acb.q8_0_to_tiles(W, N, K) if N % 16 == 0 else None
+        for form, WW, wt in (("gguf", W, acb.Q8_0), ("tiles", Wt, acb.Q8_0_TILES)):
+            if WW is None:
+                continue
+            for _ in range(3):
+                acb.gemv(WW, wt, N, K, x, y=y)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                acb.gemv(WW, wt, N, K, x, y=y)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            res[form] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1)}
+        out["shapes"][name] = res
+        del W, Wt
     return out
 
 
