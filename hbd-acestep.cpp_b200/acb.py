@@ -92,6 +92,7 @@ def lib():
             "acb_qw3lm_build_partial_head": (I, [P, I]),
             "acb_qw3lm_kv_pos": (I, [P, I]),
             "acb_qw3lm_weight_bytes": (C.c_size_t, [P]),
+            "acb_qw3lm_persistent_decode": (I, [P]),
             "acb_qw3lm_generate_greedy": (I, [P, P, I, I, I, P, P, P]),
             "acb_qw3lm_free": (None, [P]),
             "acb_qwen3_load_text_encoder": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
@@ -357,6 +358,10 @@ class QW3LM:
 
     def kv_pos(self, s=0) -> int:
         return lib().acb_qw3lm_kv_pos(self.h, s)
+
+    def persistent_decode(self) -> bool:
+        """True when single-sequence decode runs as one persistent launch per token."""
+        return bool(lib().acb_qw3lm_persistent_decode(self.h))
 
     def reset_kv(self, s=0):
         lib().acb_qw3lm_reset_kv(self.h, s)

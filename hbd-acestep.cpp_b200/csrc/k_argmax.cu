@@ -11,35 +11,10 @@
 #include <string>
 
 #include "common.cuh"
+#include "best.cuh"
 #include "ptx.cuh"
 
 namespace acb {
-
-struct Best {
-    float b1;
-    float b2;
-    int   i1;
-};
-
-__device__ __forceinline__ void best_push(Best & s, float v, int i) {
-    if (v > s.b1) {
-        s.b2 = s.b1;
-        s.b1 = v;
-        s.i1 = i;
-    } else if (v > s.b2) {
-        s.b2 = v;
-    }
-}
-
-__device__ __forceinline__ void best_merge(Best & s, float ob1, float ob2, int oi) {
-    if (ob1 > s.b1 || (ob1 == s.b1 && oi < s.i1)) {
-        s.b2 = fmaxf(s.b1, ob2);
-        s.b1 = ob1;
-        s.i1 = oi;
-    } else {
-        s.b2 = fmaxf(s.b2, ob1);
-    }
-}
 
 __device__ Best block_best(Best s) {
     __shared__ float sb1[32], sb2[32];

@@ -1,0 +1,1247 @@
+// k_decode_persist.cu -- one batch-1 greedy decode step of the Qwen3 LM (qw3lm_forward_batch with
+// N = 1, src/qwen3-lm.h:557-823, plus the temperature-0 sampler, src/sampling.h:30-34) as a
+// single persistent kernel.
+//
+// Why: at batch 1 every linear is a GEMV that moves a few MB; as separate launches each pays
+// a fill/drain of a few microseconds, and a 28-layer step issues ~200 of them. Here one CTA
+// per SM (cooperative launch) runs the whole step:
+//   - warp 8 of every CTA is a producer that streams ALL of the CTA's weight tiles for the
+//     step (each layer's qkv, o, gate|up, down slices, then the head slice) through a ring of
+//     35 KB shared-memory slots with 1-D bulk copies. Weights do not depend on activations, so
+//     the stream never waits for a layer boundary, only for a free slot;
+//   - warps 0-7 are consumers: before each GEMV they build the quantised activation in shared
+//     memory (RMSNorm * w, SwiGLU or the attention output, then Q8_0 blocks), then run a dp4a
+//     GEMV over their range of Q8_0 tiles (ACB_TYPE_Q8_0_TILES): one activation column makes
+//     the int8 MMA of k_gemv.cu a poor fit, and eight independent blocks per warp and stage
+//     keep the shared-memory ring draining at HBM rate;
+//   - a stage whose input is a whole vector written by other CTAs starts after a grid-wide
+//     barrier: one counter in global memory, release-add by each CTA, acquire-poll with a time
+//     limit. Six barriers per layer (after qkv, scores, attention, o, gate|up, down);
+//   - attention (f16 cache): CTA (kv head h, split s) normalises and rotates its q heads (and,
+//     when its split holds the new position, the new k and v, written to the cache), writes
+//     scores and the split maximum; after a barrier it forms the f16 probabilities with the
+//     global maximum and double sum, its partial P.V, and the last split CTA of the head adds
+//     the partials in split order (ticket counter);
+//   - the head GEMV keeps a running (best, second, index) per output row lane; CTAs merge
+//     theirs, and the last CTA to finish (ticket) writes the token, its margin and history,
+//     advances the position and returns the counters to zero for the next step.
+// Every wait is bounded. A CTA that gives up sets ACB_DEVERR_TIMEOUT and the barrier word's
+// abort bit; every CTA then leaves at its next barrier, and each producer waits for its own
+// copies in flight before its CTA exits.
+//
+// Arithmetic per op is that of the per-op kernels: activation quantisation of quantize_q8_0,
+// the per-block scaled int8 MMA of gemv_tiles_kernel, q/k-norm + RoPE of qkv_post_kernel, the
+// two-pass f16-cache softmax of attn_scores_kernel / attn_pv_kernel, the argmax of
+// argmax_kernel. Only the partition (16 warps, split count, tile ranges) decides summation
+// orders, as it does there.
+#include <cstdlib>
+#include <string>
+
+#include "best.cuh"
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace acb {
+
+void set_last_error(const std::string & e);
+
+namespace {
+
+constexpr int      kPdWarps       = 8;   // consumer warps
+constexpr int      kPdThreads     = (kPdWarps + 1) * 32;
+constexpr int      kPdCons        = kPdWarps * 32;
+constexpr int      kPdTileBlk     = 544;  // one 16-row x 32-column block of ACB_TYPE_Q8_0_TILES
+constexpr int      kPdStageBlocks = 64;
+constexpr int      kPdSlot        = kPdStageBlocks * kPdTileBlk;  // 34816 bytes: one K=2048 tile
+constexpr int      kPdMaxSlots    = 16;
+constexpr int      kPdBpw         = kPdStageBlocks / kPdWarps;  // blocks per warp per stage
+constexpr int      kPdMaxK        = 12288;
+constexpr int      kPdMaxChunks   = kPdMaxK / 4 / kPdCons;  // float4 activation chunks per thread
+constexpr int      kPdMaxSplit    = 32;
+constexpr int      kPdD           = 128;
+constexpr unsigned kAbortBit      = 0x80000000u;
+constexpr uint64_t kBarrierNs     = 2000000000ull;  // grid barrier time limit
+
+// shared-memory map (bytes)
+constexpr int kSmFull   = 0;     // uint64 full[16]
+constexpr int kSmEmpty  = 128;   // uint64 empty[16]
+constexpr int kSmRed    = 256;   // double [16][4]
+constexpr int kSmMisc   = 768;   // float inv[4], int flags
+constexpr int kSmTred   = 1024;  // float [2][16 warps][16 rows]
+constexpr int kSmAct    = 3072;  // int8 xq[kPdMaxK] + float xd[kPdMaxK/32]; attention scratch
+constexpr int kSmRing   = (kSmAct + kPdMaxK + kPdMaxK / 32 * 4 + 127) / 128 * 128;
+// attention scratch inside the activation region
+constexpr int kAtQ      = 0;      // float [G][128] f16-rounded q
+constexpr int kAtKp     = 2048;   // float [128] the new k (f16-rounded)
+constexpr int kAtAcc    = 2560;   // float4 [16 warps][32]
+constexpr int kAtMax    = 10752;  // float [16][G]
+
+extern __shared__ __align__(128) uint8_t pd_smem[];
+
+// shared-memory regions at constant offsets (no registers held for them)
+__device__ __forceinline__ uint64_t * sm_full() { return reinterpret_cast<uint64_t *>(pd_smem + kSmFull); }
+__device__ __forceinline__ uint64_t * sm_empty() { return reinterpret_cast<uint64_t *>(pd_smem + kSmEmpty); }
+__device__ __forceinline__ double * sm_red() { return reinterpret_cast<double *>(pd_smem + kSmRed); }
+__device__ __forceinline__ float * sm_misc() { return reinterpret_cast<float *>(pd_smem + kSmMisc); }
+__device__ __forceinline__ volatile int * sm_abort() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 32); }
+__device__ __forceinline__ volatile int * sm_last() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 36); }
+__device__ __forceinline__ float * sm_tred() { return reinterpret_cast<float *>(pd_smem + kSmTred); }
+__device__ __forceinline__ uint8_t * sm_act() { return pd_smem + kSmAct; }
+__device__ __forceinline__ int8_t * sm_xq() { return reinterpret_cast<int8_t *>(pd_smem + kSmAct); }
+__device__ __forceinline__ float * sm_xd() { return reinterpret_cast<float *>(pd_smem + kSmAct + kPdMaxK); }
+__device__ __forceinline__ uint8_t * sm_ring() { return pd_smem + kSmRing; }
+
+struct PdParams {
+    acb_decode_step s;
+    int             n_ctas, n_split, slots;
+    int             bs_h, bs_q, bs_f;  // K-blocks per ring stage at K = hidden, Nh*D, ffn
+    int64_t         prefetch;          // L2 prefetch distance (bytes) ahead of the ring stage
+    float *         hidden;
+    float *         qkv;
+    float *         scores;  // [Nh][max_seq]
+    float *         smax;    // [Nh][kPdMaxSplit]
+    float *         part;    // [kPdMaxSplit][Nh][D]
+    float *         att;     // [Nh*D]
+    float *         gu;      // [2F]
+    float4 *        bpart;   // [n_ctas]
+    unsigned *      bar;
+    int *           done;
+    int *           tickets;  // [Nkv]
+};
+
+struct ScratchMap {
+    size_t hidden, qkv, scores, smax, part, att, gu, bpart, total;
+};
+
+ScratchMap scratch_map(const acb_decode_step & s, int n_ctas) {
+    auto     al = [](size_t v) { return (v + 255) / 256 * 256; };
+    ScratchMap m{};
+    size_t   o = 256;  // bar, done, tickets[Nkv]
+    const size_t qd = (size_t) s.n_heads * s.head_dim, kvd = (size_t) s.n_kv_heads * s.head_dim;
+    m.hidden = o;
+    o        = al(o + 4 * (size_t) s.hidden);
+    m.qkv    = o;
+    o        = al(o + 4 * (qd + 2 * kvd));
+    m.scores = o;
+    o        = al(o + 4 * (size_t) s.n_heads * s.max_seq);
+    m.smax   = o;
+    o        = al(o + 4 * (size_t) s.n_heads * kPdMaxSplit);
+    m.part   = o;
+    o        = al(o + 4 * (size_t) kPdMaxSplit * qd);
+    m.att    = o;
+    o        = al(o + 4 * qd);
+    m.gu     = o;
+    o        = al(o + 4 * 2 * (size_t) s.ffn);
+    m.bpart  = o;
+    o        = al(o + 16 * (size_t) n_ctas);
+    m.total  = o;
+    return m;
+}
+
+__device__ __forceinline__ void cons_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kPdCons) : "memory");
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float f16r(float v) {
+    return __half2float(__float2half_rn(v));
+}
+
+// Balanced tile range of CTA c for GEMV number gi; the assignment rotates with gi so that the
+// CTAs holding one more tile differ from GEMV to GEMV.
+__device__ __forceinline__ void pd_range(int64_t n_tiles, int gi, int c, int G, int64_t & t0, int64_t & t1) {
+    const int v = (c + (int) (((int64_t) gi * 37) % G)) % G;
+    t0          = (int64_t) v * n_tiles / G;
+    t1          = (int64_t) (v + 1) * n_tiles / G;
+}
+
+// ---- producer: the CTA's whole weight stream of the step -----------------------------------
+// Byte range of this CTA's tiles of GEMV k of the step (k = 4 l + {qkv, o, gate|up, down};
+// k = 4 n_layers is the head); tiles of a range are contiguous, blocks in K order.
+__device__ void pd_segment(const PdParams & P, int k, const uint8_t *& ptr, int64_t & bytes, int & K, int & bs) {
+    const acb_decode_step & S  = P.s;
+    const int               qd = S.n_heads * S.head_dim;
+    const uint8_t *         W;
+    int64_t                 n_rows;
+    if (k == 4 * S.n_layers) {
+        W      = (const uint8_t *) S.head;
+        n_rows = S.vocab;
+        K      = S.hidden;
+        bs     = P.bs_h;
+    } else {
+        const acb_decode_layer & L = S.layers[k >> 2];
+        switch (k & 3) {
+            case 0:
+                W      = (const uint8_t *) L.qkv;
+                n_rows = qd + 2 * S.n_kv_heads * S.head_dim;
+                K      = S.hidden;
+                bs     = P.bs_h;
+                break;
+            case 1:
+                W      = (const uint8_t *) L.o;
+                n_rows = S.hidden;
+                K      = qd;
+                bs     = P.bs_q;
+                break;
+            case 2:
+                W      = (const uint8_t *) L.gate_up;
+                n_rows = 2 * (int64_t) S.ffn;
+                K      = S.hidden;
+                bs     = P.bs_h;
+                break;
+            default:
+                W      = (const uint8_t *) L.down;
+                n_rows = S.hidden;
+                K      = S.ffn;
+                bs     = P.bs_f;
+                break;
+        }
+    }
+    int64_t t0, t1;
+    pd_range(n_rows / 16, k, blockIdx.x, P.n_ctas, t0, t1);
+    const int64_t tile_bytes = (int64_t) (K / 32) * kPdTileBlk;
+    ptr                      = W + t0 * tile_bytes;
+    bytes                    = (t1 - t0) * tile_bytes;
+}
+
+// The producer thread: ring stages in consumption order, and ahead of them L2 prefetches of
+// the same byte stream (P.prefetch bytes ahead of the stage being issued), so that HBM keeps
+// streaming while the consumers sit at a grid barrier or in a prologue.
+__device__ void pd_producer(const PdParams & P) {
+    uint64_t *     full    = sm_full();
+    uint64_t *     empty   = sm_empty();
+    uint8_t *      ring    = sm_ring();
+    volatile int * s_abort = sm_abort();
+    const acb_decode_step & S     = P.s;
+    const uint64_t          pol   = ptx::policy_evict_first();
+    const int               nseg  = 4 * S.n_layers + 1;
+    uint32_t                it    = 0;
+    bool                    ok    = true;
+    // prefetch cursor
+    int             pk = 0, pK, pbs;
+    int64_t         po = 0, pb, pref = 0, loaded = 0;
+    const uint8_t * pp;
+    pd_segment(P, 0, pp, pb, pK, pbs);
+    for (int k = 0; k < nseg && ok; k++) {
+        const uint8_t * W;
+        int64_t         seg_bytes;
+        int             K, bs;
+        pd_segment(P, k, W, seg_bytes, K, bs);
+        const uint32_t bytes = (uint32_t) bs * kPdTileBlk;
+        for (int64_t off = 0; off < seg_bytes && ok; off += bytes) {
+            while (pref < loaded + P.prefetch && pk < nseg) {
+                if (po >= pb) {
+                    if (++pk < nseg) {
+                        pd_segment(P, pk, pp, pb, pK, pbs);
+                        po = 0;
+                    }
+                    continue;
+                }
+                const uint32_t n = (uint32_t) min((int64_t) 32768, pb - po);
+                ptx::bulk_prefetch_l2(pp + po, n);
+                po += n;
+                pref += n;
+            }
+            const int s = (int) (it % (uint32_t) P.slots);
+            if (it >= (uint32_t) P.slots) {
+                const uint32_t par = ((it / (uint32_t) P.slots) - 1) & 1;
+                uint32_t       n   = 0;
+                while (!ptx::mbar_try_wait(&empty[s], par)) {
+                    if (*s_abort) {
+                        ok = false;
+                        break;
+                    }
+                    if (++n > (1u << 24)) {
+                        if (S.err) {
+                            atomicOr(S.err, ACB_DEVERR_TIMEOUT);
+                        }
+                        atomicOr(P.bar, kAbortBit);
+                        ok = false;
+                        break;
+                    }
+                }
+                if (!ok) {
+                    break;
+                }
+            }
+            ptx::mbar_arrive_expect_tx(&full[s], bytes);
+            ptx::bulk_g2s_stream(ring + (size_t) s * kPdSlot, W + off, bytes, &full[s], pol);
+            it++;
+            loaded += bytes;
+        }
+    }
+    if (!ok) {
+        // the consumers stopped: wait (bounded) for the copies this thread still has in flight
+        const uint32_t first = it > (uint32_t) P.slots ? it - (uint32_t) P.slots : 0;
+        for (uint32_t i = first; i < it; i++) {
+            ptx::mbar_wait(&full[i % (uint32_t) P.slots], (i / (uint32_t) P.slots) & 1);
+        }
+    }
+}
+
+// ---- consumer pieces --------------------------------------------------------------------------
+struct PdCtx {
+    uint32_t it;     // ring stage counter (the producer's issue order)
+    int      tbuf;   // tile-reduction buffer parity
+    unsigned epoch;  // grid barriers passed
+};
+
+// Grid-wide barrier over the consumers of every CTA. Returns false when the step is aborted.
+__device__ bool pd_grid_sync(const PdParams & P, PdCtx & x) {
+    cons_sync();
+    x.epoch++;
+    if (threadIdx.x == 0) {
+        const unsigned target = x.epoch * (unsigned) P.n_ctas;
+        __threadfence();
+        unsigned v = *sm_abort() ? (atomicOr(P.bar, kAbortBit) | kAbortBit) : atomicAdd(P.bar, 1u) + 1u;
+        if (!(v & kAbortBit) && v < target) {
+            const uint64_t t0 = globaltimer();
+            for (;;) {
+                v = ld_acquire(P.bar);
+                if ((v & kAbortBit) || (v & ~kAbortBit) >= target) {
+                    break;
+                }
+                if (globaltimer() - t0 > kBarrierNs) {
+                    if (P.s.err) {
+                        atomicOr(P.s.err, ACB_DEVERR_TIMEOUT);
+                    }
+                    atomicOr(P.bar, kAbortBit);
+                    v |= kAbortBit;
+                    break;
+                }
+            }
+        }
+        if (v & kAbortBit) {
+            *sm_abort() = 1;
+        }
+        __threadfence();
+    }
+    cons_sync();
+    return *sm_abort() == 0;
+}
+
+// Wait for ring stage s; false once the step is aborted (then the caller skips the stage's
+// work but keeps every named barrier, so all consumer warps reach the next grid barrier).
+__device__ __forceinline__ bool pd_wait_full(const PdParams & P, PdCtx & x, int s, uint32_t par) {
+    if (*sm_abort()) {
+        return false;
+    }
+    if (ptx::mbar_wait(&sm_full()[s], par)) {
+        return true;
+    }
+    if ((threadIdx.x & 31) == 0) {
+        if (P.s.err) {
+            atomicOr(P.s.err, ACB_DEVERR_TIMEOUT);
+        }
+        atomicOr(P.bar, kAbortBit);
+        *sm_abort() = 1;
+    }
+    return false;
+}
+
+enum { ACT_X = 0, ACT_RMS = 1, ACT_SWIGLU = 2, ACT_EMBED = 3 };
+
+// Activation of K elements -> Q8_0 blocks in shared memory (quantize_q8_0 arithmetic). Thread t
+// owns float4 chunks t, t + 512, ...; the 8 chunks of a 32-element block sit in 8 adjacent lanes.
+// All loads (activation and norm gains) are issued before the first use.
+template <int MODE, int NCH>
+__device__ void pd_act_quant_n(const PdParams & P, PdCtx & x, const float * src, const float * w,
+                               const uint8_t * erow, int K, float * raw_out) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int nf  = K / 4;
+    float4    v[NCH], ww[NCH];
+#pragma unroll
+    for (int i = 0; i < NCH; i++) {
+        // loads at a clamped index, then a select (predicated loads cost registers)
+        const int f  = tid + i * kPdCons;
+        const int fc = min(f, nf - 1);
+        ww[i]        = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+        if ((MODE == ACT_RMS || MODE == ACT_EMBED) && w) {
+            ww[i] = __ldg(reinterpret_cast<const float4 *>(w) + fc);
+        }
+        {
+            const int f = fc;
+            if (MODE == ACT_EMBED) {
+                const uint8_t * b = erow + (f >> 3) * 34;
+                const float     d = f16_bits_to_f(ld_u16(b));
+                const int8_t *  q = reinterpret_cast<const int8_t *>(b + 2 + (f & 7) * 4);
+                v[i] = make_float4(__fmul_rn(d, (float) q[0]), __fmul_rn(d, (float) q[1]), __fmul_rn(d, (float) q[2]),
+                                   __fmul_rn(d, (float) q[3]));
+                if (raw_out) {
+                    reinterpret_cast<float4 *>(raw_out)[f] = v[i];
+                }
+            } else if (MODE == ACT_SWIGLU) {
+                const float4 g = __ldcg(reinterpret_cast<const float4 *>(src) + f);
+                const float4 u = __ldcg(reinterpret_cast<const float4 *>(src + K) + f);
+                v[i] = make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z),
+                                   silu_times(g.w, u.w));
+            } else {
+                v[i] = __ldcg(reinterpret_cast<const float4 *>(src) + f);
+            }
+        }
+        if (f >= nf) {
+            v[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+    }
+    if (MODE == ACT_RMS || MODE == ACT_EMBED) {
+        double ss = 0.0;
+#pragma unroll
+        for (int i = 0; i < NCH; i++) {
+            ss += (double) __fmul_rn(v[i].x, v[i].x);
+            ss += (double) __fmul_rn(v[i].y, v[i].y);
+            ss += (double) __fmul_rn(v[i].z, v[i].z);
+            ss += (double) __fmul_rn(v[i].w, v[i].w);
+        }
+        ss = warp_sum(ss);
+        if (lane == 0) {
+            sm_red()[tid >> 5] = ss;
+        }
+        cons_sync();
+        double t = 0.0;
+        for (int i = 0; i < kPdWarps; i++) {
+            t += sm_red()[i];
+        }
+        const float sc = rms_scale(t, K, P.s.eps);
+#pragma unroll
+        for (int i = 0; i < NCH; i++) {
+            v[i].x = __fmul_rn(v[i].x, sc);
+            v[i].y = __fmul_rn(v[i].y, sc);
+            v[i].z = __fmul_rn(v[i].z, sc);
+            v[i].w = __fmul_rn(v[i].w, sc);
+            if (w) {
+                v[i].x = __fmul_rn(v[i].x, ww[i].x);
+                v[i].y = __fmul_rn(v[i].y, ww[i].y);
+                v[i].z = __fmul_rn(v[i].z, ww[i].z);
+                v[i].w = __fmul_rn(v[i].w, ww[i].w);
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NCH; i++) {
+        if (i * kPdCons >= nf) {
+            break;  // uniform over the CTA
+        }
+        const int f    = tid + i * kPdCons;
+        float     amax = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+        amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        if (f < nf) {
+            const float d  = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            const int   q0 = (int) roundf(__fmul_rn(v[i].x, id));
+            const int   q1 = (int) roundf(__fmul_rn(v[i].y, id));
+            const int   q2 = (int) roundf(__fmul_rn(v[i].z, id));
+            const int   q3 = (int) roundf(__fmul_rn(v[i].w, id));
+            // words of a block stored in the order 0,4,1,5,2,6,3,7: the GEMV lane q reads its
+            // words q and 4 + q as one 8-byte load
+            const int w = f & 7;
+            reinterpret_cast<uint32_t *>(sm_xq())[(f & ~7) + ((w & 3) << 1) + (w >> 2)] =
+                (uint32_t) (q0 & 0xff) | ((uint32_t) (q1 & 0xff) << 8) | ((uint32_t) (q2 & 0xff) << 16) |
+                ((uint32_t) (q3 & 0xff) << 24);
+            if ((f & 7) == 0) {
+                sm_xd()[f >> 3] = __half2float(__float2half_rn(d));
+            }
+        }
+    }
+    cons_sync();
+}
+
+template <int MODE>
+__device__ __forceinline__ void pd_act_quant(const PdParams & P, PdCtx & x, const float * src, const float * w,
+                                             const uint8_t * erow, int K, float * raw_out) {
+    if (K <= kPdCons * 8) {
+        pd_act_quant_n<MODE, 2>(P, x, src, w, erow, K, raw_out);
+    } else if (K <= kPdCons * 16) {
+        pd_act_quant_n<MODE, 4>(P, x, src, w, erow, K, raw_out);
+    } else {
+        pd_act_quant_n<MODE, kPdMaxChunks>(P, x, src, w, erow, K, raw_out);
+    }
+}
+
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_HEAD = 2 };
+
+// One 16-row x 32-column tile block for one activation column. Lane 4g + q holds bytes
+// 4q..4q+3 and 16+4q..16+4q+3 of rows g and g + 8 (the tile order) and the activation words q
+// and 4 + q (xw); two dp4a per row give its integer partial sum over those 8 columns, scaled by
+// d_w * d_x of the block into the lane's float partials of the two rows.
+__device__ __forceinline__ void pd_block(const uint4 & a, uint32_t dw, uint2 xw, float dx, float & acc0,
+                                         float & acc2) {
+    const int   s0 = __dp4a((int) a.z, (int) xw.y, __dp4a((int) a.x, (int) xw.x, 0));
+    const int   s1 = __dp4a((int) a.w, (int) xw.y, __dp4a((int) a.y, (int) xw.x, 0));
+    const float dl = f16_bits_to_f((uint16_t) (dw & 0xffff));
+    const float dh = f16_bits_to_f((uint16_t) (dw >> 16));
+    acc0           = __fmaf_rn((float) s0, __fmul_rn(dl, dx), acc0);
+    acc2           = __fmaf_rn((float) s1, __fmul_rn(dh, dx), acc2);
+}
+
+// Tensor-core Q8_0 tile GEMV over this CTA's tile range (gemv_tiles_kernel arithmetic for one
+// activation column): warp w takes blocks w, w + 16, ... of every stage; at the end of a tile
+// the 16 warps' partials are added in warp order by one warp (rotating) and stored.
+template <int EPI>
+__device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n_rows, int K, int bs, int gi, float * y, Best & best) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, q = lane & 3;
+    int64_t   t0, t1;
+    pd_range(n_rows / 16, gi, blockIdx.x, P.n_ctas, t0, t1);
+    const int        nb  = K / 32;
+    const uint32_t * xq4 = reinterpret_cast<const uint32_t *>(sm_xq());
+    for (int64_t t = t0; t < t1; t++) {
+        float acc0 = 0.0f, acc2 = 0.0f;  // rows g and g + 8, this lane's 8 of every 32 columns
+        for (int b0 = 0; b0 < nb; b0 += bs) {
+            const int       s    = (int) (x.it % (uint32_t) P.slots);
+            const bool      have = pd_wait_full(P, x, s, (x.it / (uint32_t) P.slots) & 1);
+            const uint8_t * st   = sm_ring() + (size_t) s * kPdSlot;
+            // warp w takes nbw consecutive blocks of the stage; every shared-memory operand of
+            // its blocks is loaded first. Lane 4g + q holds bytes 4q..4q+3 and 16+4q..16+4q+3 of
+            // rows g and g + 8 (the tile order); its two dp4a pairs give those rows' partial sums
+            // over its 8 columns, scaled per block (d_w * d_x) into per-lane float partials
+            // that are added over the 4 lanes of a row at the end of the tile.
+            const int nbw = (bs + kPdWarps - 1) / kPdWarps, bw0 = warp * nbw;
+            if (nbw == kPdBpw && bw0 + kPdBpw <= bs && (b0 & 3) == 0) {
+                // all of this warp's blocks are in the stage: constant offsets (the scales of
+                // blocks bb.. are read as 16-byte aligned float4: bb is a multiple of 4)
+                const uint8_t * sp = st + bw0 * kPdTileBlk;
+                const int       bb = b0 + bw0;
+                uint4           a[kPdBpw];
+                uint32_t        dw[kPdBpw];
+                uint2           xw[kPdBpw];
+#pragma unroll
+                for (int u = 0; u < kPdBpw; u++) {
+                    a[u]  = *reinterpret_cast<const uint4 *>(sp + u * kPdTileBlk + lane * 16);
+                    dw[u] = *reinterpret_cast<const uint32_t *>(sp + u * kPdTileBlk + 512 + g * 4);
+                    xw[u] = *reinterpret_cast<const uint2 *>(xq4 + 8 * (bb + u) + 2 * q);
+                }
+                float dx[kPdBpw];
+#pragma unroll
+                for (int u = 0; u < kPdBpw; u += 4) {
+                    const float4 d4 = *reinterpret_cast<const float4 *>(sm_xd() + bb + u);
+                    dx[u]           = d4.x;
+                    dx[u + 1]       = d4.y;
+                    dx[u + 2]       = d4.z;
+                    dx[u + 3]       = d4.w;
+                }
+                if (have) {
+#pragma unroll
+                    for (int u = 0; u < kPdBpw; u++) {
+                        pd_block(a[u], dw[u], xw[u], dx[u], acc0, acc2);
+                    }
+                }
+            } else {
+                // ragged stage: indices past it are clamped to its last block (loads stay
+                // unconditional: a predicated load sequence costs registers) and skipped
+#pragma unroll
+                for (int u = 0; u < kPdBpw; u++) {
+                    const int   bl = min(bw0 + u, bs - 1);
+                    const int   b  = b0 + bl;
+                    const uint4 a  = *reinterpret_cast<const uint4 *>(st + bl * kPdTileBlk + lane * 16);
+                    const uint32_t dw = *reinterpret_cast<const uint32_t *>(st + bl * kPdTileBlk + 512 + g * 4);
+                    const uint2 xw = *reinterpret_cast<const uint2 *>(xq4 + 8 * b + 2 * q);
+                    const float dx = sm_xd()[b];
+                    if (have && u < nbw && bw0 + u < bs) {
+                        pd_block(a, dw, xw, dx, acc0, acc2);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0 && have) {
+                ptx::mbar_arrive(&sm_empty()[s]);
+            }
+            x.it++;
+        }
+        acc0 = __fadd_rn(acc0, __shfl_xor_sync(0xffffffffu, acc0, 1));
+        acc2 = __fadd_rn(acc2, __shfl_xor_sync(0xffffffffu, acc2, 1));
+        acc0 = __fadd_rn(acc0, __shfl_xor_sync(0xffffffffu, acc0, 2));
+        acc2 = __fadd_rn(acc2, __shfl_xor_sync(0xffffffffu, acc2, 2));
+        float * tr = sm_tred() + x.tbuf * (kPdWarps * 16);
+        if (q == 0) {
+            tr[warp * 16 + g]     = acc0;
+            tr[warp * 16 + g + 8] = acc2;
+        }
+        cons_sync();
+        if (warp == (int) ((t - t0) & (kPdWarps - 1)) && lane < 16) {
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kPdWarps; w++) {
+                v = __fadd_rn(v, tr[w * 16 + lane]);
+            }
+            const int64_t row = t * 16 + lane;
+            if (EPI == EPI_ADD) {
+                y[row] = __fadd_rn(__ldcg(y + row), v);
+            } else {
+                y[row] = v;
+            }
+            if (EPI == EPI_HEAD) {
+                best_push(best, v, (int) row);
+            }
+        }
+        x.tbuf ^= 1;
+    }
+    return *sm_abort() == 0;
+}
+
+// q/k RMSNorm (per head, D = 128) and NeoX RoPE of one head by one warp (qkv_post_kernel with
+// E = 2): lane owns elements 2*lane + e (a) and 64 + 2*lane + e (b).
+__device__ __forceinline__ void pd_norm_rope(const float * src, const float * w, float eps, const float * rope_row,
+                                             float a[2], float b[2]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        a[e] = __ldcg(src + lane * 2 + e);
+        b[e] = __ldcg(src + 64 + lane * 2 + e);
+    }
+    if (w) {
+        double ss = 0.0;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            ss += (double) __fmul_rn(a[e], a[e]);
+            ss += (double) __fmul_rn(b[e], b[e]);
+        }
+        ss             = warp_sum(ss);
+        const float sc = rms_scale(ss, kPdD, eps);
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * 2 + e));
+            b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(w + 64 + lane * 2 + e));
+        }
+    }
+    const float * cs = rope_row + 4 * lane;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const float c = __ldg(cs + 2 * e), s = __ldg(cs + 2 * e + 1);
+        const float x0 = a[e], x1 = b[e];
+        a[e]           = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        b[e]           = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+    }
+}
+
+// Split count of the attention at kv length n: one split per 64 keys, at most one CTA per
+// (kv head, split) and kPdMaxSplit. Both passes of a step derive the same value.
+__device__ __forceinline__ int pd_splits(const PdParams & P, int n) {
+    return min(P.n_split, max(1, (n + 63) / 64));
+}
+
+// Attention pass 1 for CTA (kv head h, split s): q heads of the group, the new k/v (by the
+// split that holds position p), scores of the split's keys and the split maximum. The split's
+// first keys are requested before the q/k work so that their latency overlaps it; key p reads
+// the new k from shared memory.
+template <int G>
+__device__ void pd_attn_scores(const PdParams & P, PdCtx & x, const acb_decode_layer & L, int p) {
+    const acb_decode_step & S = P.s;
+    const int               c = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int               kv_len = p + 1, ns = pd_splits(P, kv_len);
+    if (c >= S.n_kv_heads * ns) {
+        return;
+    }
+    const int     h = c / ns, sp = c % ns, Nh = S.n_heads, Nkv = S.n_kv_heads;
+    const int     chunk = (kv_len + ns - 1) / ns;
+    const int     j0 = sp * chunk, j1 = min(kv_len, j0 + chunk);
+    const int64_t base = ((int64_t) S.kv_set * Nkv + h) * S.max_seq * kPdD;
+    uint16_t *    kb   = L.k_cache + base;
+    uint16_t *    vb   = L.v_cache + base;
+    float *       qf   = reinterpret_cast<float *>(sm_act() + kAtQ);
+    float *       kp   = reinterpret_cast<float *>(sm_act() + kAtKp);
+    float *       wmax = reinterpret_cast<float *>(sm_act() + kAtMax);
+    const float * rope = S.rope + (int64_t) p * kPdD;
+    // 8 lanes per key: lane owns dims [16 sub, 16 sub + 16) of key slot ks (attn_scores_kernel);
+    // U groups of 4 keys per warp in flight
+    constexpr int U   = 2;
+    const int     sub = lane & 7, ks = lane >> 3;
+    uint4         raw[U][2];
+    auto          load_keys = [&](int jb) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int     j   = min(jb + kPdWarps * 4 * u + ks, j1 - 1);  // clamped: scored only if in range
+            const uint4 * src = reinterpret_cast<const uint4 *>(kb + (int64_t) j * kPdD + 16 * sub);
+            raw[u][0]         = __ldcg(src);
+            raw[u][1]         = __ldcg(src + 1);
+        }
+    };
+    int jb = j0 + warp * 4;
+    load_keys(jb);
+    const bool own_p = p >= j0 && p < j1;
+    if (warp < G) {
+        float a[2], b[2];
+        pd_norm_rope(P.qkv + (int64_t) (h * G + warp) * kPdD, L.q_norm, S.eps, rope, a, b);
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            qf[warp * kPdD + 2 * lane + e]      = f16r(a[e]);
+            qf[warp * kPdD + 64 + 2 * lane + e] = f16r(b[e]);
+        }
+    } else if (warp == G && own_p) {
+        float a[2], b[2];
+        pd_norm_rope(P.qkv + (int64_t) (Nh + h) * kPdD, L.k_norm, S.eps, rope, a, b);
+        uint16_t * d = kb + (int64_t) p * kPdD;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const __half ha = __float2half_rn(a[e]), hb = __float2half_rn(b[e]);
+            d[2 * lane + e]       = __half_as_ushort(ha);
+            d[64 + 2 * lane + e]  = __half_as_ushort(hb);
+            kp[2 * lane + e]      = __half2float(ha);
+            kp[64 + 2 * lane + e] = __half2float(hb);
+        }
+    } else if (warp == G + 1 && own_p) {
+        const float * src = P.qkv + (int64_t) (Nh + Nkv + h) * kPdD;
+        uint16_t *    d   = vb + (int64_t) p * kPdD;
+        float         v[4];
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            v[e]     = __ldcg(src + 2 * lane + e);
+            v[2 + e] = __ldcg(src + 64 + 2 * lane + e);
+        }
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            d[2 * lane + e]      = __half_as_ushort(__float2half_rn(v[e]));
+            d[64 + 2 * lane + e] = __half_as_ushort(__float2half_rn(v[2 + e]));
+        }
+        __threadfence();  // read back by pass 2 of this CTA through L2
+    }
+    cons_sync();
+    float qv[G][16];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+#pragma unroll
+        for (int e = 0; e < 16; e++) {
+            qv[g][e] = qf[g * kPdD + 16 * sub + e];
+        }
+    }
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        mx[g] = -INFINITY;
+    }
+    for (;;) {
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = jb + kPdWarps * 4 * u + ks;
+            float     kf[16];
+            if (j == p) {
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    kf[e] = kp[16 * sub + e];
+                }
+            } else {
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const __half2 * hp = reinterpret_cast<const __half2 *>(&raw[u][hh]);
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float2 f        = __half22float2(hp[e]);
+                        kf[8 * hh + 2 * e]     = f.x;
+                        kf[8 * hh + 2 * e + 1] = f.y;
+                    }
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    acc = __fadd_rn(acc, __fmul_rn(kf[e], qv[g][e]));
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+                const float sv = __fmul_rn(acc, S.attn_scale);
+                if (j < j1) {
+                    if (sub == 0) {
+                        P.scores[(int64_t) (h * G + g) * S.max_seq + j] = sv;
+                    }
+                    mx[g] = fmaxf(mx[g], sv);
+                }
+            }
+        }
+        jb += kPdWarps * 4 * U;
+        if (jb >= j1) {
+            break;
+        }
+        load_keys(jb);
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        mx[g] = warp_max(mx[g]);
+    }
+    if (lane == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            wmax[warp * G + g] = mx[g];
+        }
+    }
+    cons_sync();
+    if (threadIdx.x < G) {
+        float m = -INFINITY;
+        for (int w = 0; w < kPdWarps; w++) {
+            m = fmaxf(m, wmax[w * G + threadIdx.x]);
+        }
+        P.smax[(int64_t) (h * G + threadIdx.x) * kPdMaxSplit + sp] = m;
+    }
+}
+
+// Attention pass 2 for CTA (h, s): global max and double sum of the group's rows, f16
+// probabilities of the split's keys, partial P.V; the last split CTA of the head adds the
+// partials in split order into the attention output. Every loop over memory keeps its loads
+// in flight together (a dependent chain of L2 round trips would dominate the step).
+template <int G>
+__device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer & L, int p) {
+    const acb_decode_step & S = P.s;
+    const int               c = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int               kv_len = p + 1, ns = pd_splits(P, kv_len);
+    if (c >= S.n_kv_heads * ns) {
+        return;
+    }
+    constexpr int WPH = kPdWarps / G;  // warps per q head
+    constexpr int UV  = 16;            // keys in flight per warp
+    const int     h = c / ns, sp = c % ns, Nh = S.n_heads;
+    const int     chunk = (kv_len + ns - 1) / ns;
+    const int     j0 = sp * chunk, j1 = min(kv_len, j0 + chunk);
+    const uint16_t * vb = L.v_cache + ((int64_t) S.kv_set * S.n_kv_heads + h) * S.max_seq * kPdD;
+    // warp w serves q head g = w / WPH over keys j0 + (w % WPH) + WPH u; lane owns 4 dims.
+    // Its first UV keys (V rows and scores) are requested now: they do not depend on the max.
+    const int     g  = warp / WPH, wi = warp % WPH, hq = h * G + g;
+    const float * sr = P.scores + (int64_t) hq * S.max_seq;
+    uint2         vr[UV];
+    float         sv[UV];
+    auto          load_pv = [&](int jb) {
+#pragma unroll
+        for (int u = 0; u < UV; u++) {
+            const int j = max(j0, min(jb + WPH * u, j1 - 1));  // clamped: used only if in range
+            vr[u]       = __ldcg(reinterpret_cast<const uint2 *>(vb + (int64_t) j * kPdD + lane * 4));
+            sv[u]       = __ldcg(sr + j);
+        }
+    };
+    int jb = j0 + wi;
+    load_pv(jb);
+    float * sM = sm_misc() + 4;
+    if (warp < G) {
+        float m = lane < ns ? __ldcg(P.smax + (int64_t) (h * G + warp) * kPdMaxSplit + lane) : -INFINITY;
+        m       = warp_max(m);
+        if (lane == 0) {
+            sM[warp] = m;
+        }
+    }
+    cons_sync();
+    float M[G];
+#pragma unroll
+    for (int gg = 0; gg < G; gg++) {
+        M[gg] = sM[gg];
+    }
+    // sum of expf(s - M) in double over each whole row: thread t takes j = t + 512 i
+    constexpr int US = 8;
+#pragma unroll
+    for (int gg = 0; gg < G; gg++) {
+        const float * r = P.scores + (int64_t) (h * G + gg) * S.max_seq;
+        double        s = 0.0;
+        for (int j = tid; j < kv_len; j += US * kPdCons) {
+            float t[US];
+#pragma unroll
+            for (int u = 0; u < US; u++) {
+                t[u] = j + u * kPdCons < kv_len ? __ldcg(r + j + u * kPdCons) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < US; u++) {
+                if (j + u * kPdCons < kv_len) {
+                    s += (double) expf(__fsub_rn(t[u], M[gg]));
+                }
+            }
+        }
+        s = warp_sum(s);
+        if (lane == 0) {
+            sm_red()[warp * 4 + gg] = s;
+        }
+    }
+    cons_sync();
+    if (tid < G) {
+        double t = 0.0;
+        for (int w = 0; w < kPdWarps; w++) {
+            t += sm_red()[w * 4 + tid];
+        }
+        sm_misc()[tid] = t > 0.0 ? (float) (1.0 / t) : 0.0f;
+    }
+    cons_sync();
+    const float Mg = M[g], ig = sm_misc()[g];
+    float4      acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (;;) {
+#pragma unroll
+        for (int u = 0; u < UV; u++) {
+            const int j = jb + WPH * u;
+            if (j < j1) {
+                const float  pp  = f16r(__fmul_rn(expf(__fsub_rn(sv[u], Mg)), ig));
+                const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[u].x));
+                const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[u].y));
+                acc.x            = __fadd_rn(acc.x, __fmul_rn(f01.x, pp));
+                acc.y            = __fadd_rn(acc.y, __fmul_rn(f01.y, pp));
+                acc.z            = __fadd_rn(acc.z, __fmul_rn(f23.x, pp));
+                acc.w            = __fadd_rn(acc.w, __fmul_rn(f23.y, pp));
+            }
+        }
+        jb += WPH * UV;
+        if (jb >= j1) {
+            break;
+        }
+        load_pv(jb);
+    }
+    float4 * wacc = reinterpret_cast<float4 *>(sm_act() + kAtAcc);
+    wacc[warp * 32 + lane] = acc;
+    cons_sync();
+    if (wi == 0) {
+        float4 r = wacc[warp * 32 + lane];
+        for (int w = 1; w < WPH; w++) {
+            const float4 o = wacc[(warp + w) * 32 + lane];
+            r.x            = __fadd_rn(r.x, o.x);
+            r.y            = __fadd_rn(r.y, o.y);
+            r.z            = __fadd_rn(r.z, o.z);
+            r.w            = __fadd_rn(r.w, o.w);
+        }
+        __stcg(reinterpret_cast<float4 *>(P.part + ((int64_t) sp * Nh + hq) * kPdD) + lane, r);
+        __threadfence();
+    }
+    cons_sync();
+    if (tid == 0) {
+        const int tk = atomicAdd(P.tickets + h, 1);
+        *sm_last()    = (tk == ns - 1);
+    }
+    cons_sync();
+    if (!*sm_last()) {
+        return;
+    }
+    // last split CTA of the head: thread (q, g, l) adds splits [q ns / Q, (q + 1) ns / Q) in
+    // order, then the Q partial sums are added in order
+    __threadfence();
+    constexpr int Q    = kPdWarps / G;  // split ranges (G * 32 * Q == 512)
+    constexpr int QMAX = (kPdMaxSplit + Q - 1) / Q;
+    const int     q    = tid / (G * 32), gl = tid % (G * 32);
+    const int     s0   = q * ns / Q, s1 = (q + 1) * ns / Q;
+    const int64_t off  = (int64_t) (h * G) * kPdD + gl * 4;
+    float4        v[QMAX];
+#pragma unroll
+    for (int i = 0; i < QMAX; i++) {
+        const int si = min(s0 + i, ns - 1);  // clamped: added only if in the range
+        v[i]         = __ldcg(reinterpret_cast<const float4 *>(P.part + (int64_t) si * Nh * kPdD + off));
+    }
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < QMAX; i++) {
+        if (s0 + i < s1) {
+            a = i == 0 ? v[0] : make_float4(__fadd_rn(a.x, v[i].x), __fadd_rn(a.y, v[i].y), __fadd_rn(a.z, v[i].z),
+                                            __fadd_rn(a.w, v[i].w));
+        }
+    }
+    wacc[tid] = a;  // the block reduction above is complete (cons_sync after the ticket)
+    cons_sync();
+    if (tid < G * 32) {
+        float4 r  = wacc[tid];
+        bool   hv = 0 < (ns / Q);  // range 0 non-empty
+        for (int qq = 1; qq < Q; qq++) {
+            if ((qq + 1) * ns / Q > qq * ns / Q) {
+                const float4 o = wacc[qq * G * 32 + tid];
+                if (!hv) {
+                    r  = o;
+                    hv = true;
+                } else {
+                    r.x = __fadd_rn(r.x, o.x);
+                    r.y = __fadd_rn(r.y, o.y);
+                    r.z = __fadd_rn(r.z, o.z);
+                    r.w = __fadd_rn(r.w, o.w);
+                }
+            }
+        }
+        __stcg(reinterpret_cast<float4 *>(P.att + off), r);
+        if (tid == 0) {
+            P.tickets[h] = 0;
+        }
+    }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams P) {
+    const acb_decode_step & S = P.s;
+    const int               tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    PdCtx                   x;
+    x.it      = 0;
+    x.tbuf    = 0;
+    x.epoch   = 0;
+
+    // step inputs: every CTA reads the same values and takes the same exit
+    const int id = __ldcg(S.ids), p = __ldcg(S.pos);
+    if (id < 0 || id >= S.embed_rows || p < 0 || p >= S.max_seq || p >= S.max_pos) {
+        if (blockIdx.x == 0 && tid == 0 && S.err) {
+            atomicOr(S.err, (id < 0 || id >= S.embed_rows) ? ACB_DEVERR_ID_RANGE : ACB_DEVERR_POS_RANGE);
+        }
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < P.slots; s++) {
+            ptx::mbar_init(&sm_full()[s], 1);
+            ptx::mbar_init(&sm_empty()[s], kPdWarps);
+        }
+        *sm_abort() = 0;
+        *sm_last()  = 0;
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == kPdWarps) {
+        if (lane == 0) {
+            pd_producer(P);
+        }
+        return;
+    }
+
+    const int qd = S.n_heads * S.head_dim, qkvd = qd + 2 * S.n_kv_heads * S.head_dim;
+    Best      best = { -INFINITY, -INFINITY, 0x7fffffff };
+    bool      ok   = true;
+    for (int l = 0; l < S.n_layers && ok; l++) {
+        const acb_decode_layer & L = S.layers[l];
+        if (l == 0) {
+            const uint8_t * erow = (const uint8_t *) S.embed + (int64_t) id * (S.hidden / 32 * 34);
+            pd_act_quant<ACT_EMBED>(P, x, nullptr, L.attn_norm, erow, S.hidden, blockIdx.x == 0 ? P.hidden : nullptr);
+        } else {
+            pd_act_quant<ACT_RMS>(P, x, P.hidden, L.attn_norm, nullptr, S.hidden, nullptr);
+        }
+        ok = pd_gemv<EPI_STORE>(P, x, qkvd, S.hidden, P.bs_h, 4 * l, P.qkv, best) && pd_grid_sync(P, x);
+        if (!ok) {
+            break;
+        }
+        pd_attn_scores<G>(P, x, L, p);
+        if (!pd_grid_sync(P, x)) {
+            break;
+        }
+        pd_attn_pv<G>(P, x, L, p);
+        if (!pd_grid_sync(P, x)) {
+            break;
+        }
+        pd_act_quant<ACT_X>(P, x, P.att, nullptr, nullptr, qd, nullptr);
+        ok = pd_gemv<EPI_ADD>(P, x, S.hidden, qd, P.bs_q, 4 * l + 1, P.hidden, best) && pd_grid_sync(P, x);
+        if (!ok) {
+            break;
+        }
+        pd_act_quant<ACT_RMS>(P, x, P.hidden, L.post_norm, nullptr, S.hidden, nullptr);
+        ok = pd_gemv<EPI_STORE>(P, x, 2 * (int64_t) S.ffn, S.hidden, P.bs_h, 4 * l + 2, P.gu, best) &&
+             pd_grid_sync(P, x);
+        if (!ok) {
+            break;
+        }
+        pd_act_quant<ACT_SWIGLU>(P, x, P.gu, nullptr, nullptr, S.ffn, nullptr);
+        ok = pd_gemv<EPI_ADD>(P, x, S.hidden, S.ffn, P.bs_f, 4 * l + 3, P.hidden, best) && pd_grid_sync(P, x);
+    }
+    if (!ok) {
+        return;
+    }
+    pd_act_quant<ACT_RMS>(P, x, P.hidden, S.final_norm, nullptr, S.hidden, nullptr);
+    if (!pd_gemv<EPI_HEAD>(P, x, S.vocab, S.hidden, P.bs_h, 4 * S.n_layers, S.logits, best)) {
+        return;
+    }
+    // CTA best -> partial; the last CTA merges in CTA order and finishes the step
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        best_merge(best, __shfl_xor_sync(0xffffffffu, best.b1, o), __shfl_xor_sync(0xffffffffu, best.b2, o),
+                   __shfl_xor_sync(0xffffffffu, best.i1, o));
+    }
+    float4 * wb = reinterpret_cast<float4 *>(sm_act());
+    if (lane == 0) {
+        wb[warp] = make_float4(best.b1, best.b2, __int_as_float(best.i1), 0.0f);
+    }
+    cons_sync();
+    if (tid == 0) {
+        Best r = { -INFINITY, -INFINITY, 0x7fffffff };
+        for (int w = 0; w < kPdWarps; w++) {
+            const float4 v = wb[w];
+            best_merge(r, v.x, v.y, __float_as_int(v.z));
+        }
+        __stcg(P.bpart + blockIdx.x, make_float4(r.b1, r.b2, __int_as_float(r.i1), 0.0f));
+        __threadfence();
+        const int tk = atomicAdd(P.done, 1);
+        *sm_last()    = (tk == P.n_ctas - 1);
+    }
+    cons_sync();
+    if (!*sm_last() || warp != 0) {
+        return;
+    }
+    __threadfence();
+    Best r = { -INFINITY, -INFINITY, 0x7fffffff };
+    for (int k = lane; k < P.n_ctas; k += 32) {
+        const float4 v = __ldcg(P.bpart + k);
+        best_merge(r, v.x, v.y, __float_as_int(v.z));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        best_merge(r, __shfl_xor_sync(0xffffffffu, r.b1, o), __shfl_xor_sync(0xffffffffu, r.b2, o),
+                   __shfl_xor_sync(0xffffffffu, r.i1, o));
+    }
+    if (lane == 0) {
+        if (S.greedy) {
+            S.ids[0] = r.i1;
+            if (S.margin) {
+                S.margin[0] = r.b1 - r.b2;
+            }
+            if (S.hist && S.hist_base) {
+                const int step = p - S.hist_base[0];
+                S.hist[step]   = r.i1;
+                if (S.mhist) {
+                    S.mhist[step] = r.b1 - r.b2;
+                }
+            }
+            S.pos[0] = p + 1;
+        }
+        // every CTA has passed its last barrier: the counters return to zero for the next step
+        *P.done = 0;
+        *P.bar  = 0;
+    }
+}
+
+int blocks_per_stage(int K) {
+    const int nb = K / 32;
+    int       bs = 1;
+    for (int d = 1; d <= kPdStageBlocks && d <= nb; d++) {
+        if (nb % d == 0) {
+            bs = d;
+        }
+    }
+    return bs;
+}
+
+const char * check_shape(const acb_decode_step & s) {
+    if (s.head_dim != kPdD) {
+        return "head_dim must be 128";
+    }
+    if (s.n_layers <= 0 || s.n_kv_heads <= 0 || s.n_heads % s.n_kv_heads != 0) {
+        return "bad layer or head counts";
+    }
+    const int G = s.n_heads / s.n_kv_heads;
+    if (G != 1 && G != 2 && G != 4) {
+        return "q heads per kv head must be 1, 2 or 4";
+    }
+    if (s.n_kv_heads > 48) {
+        return "too many kv heads";
+    }
+    const int qd = s.n_heads * kPdD;
+    for (int k : { s.hidden, s.ffn, qd }) {
+        if (k <= 0 || k % 32 != 0 || k > kPdMaxK) {
+            return "hidden, ffn and Nh*D must be multiples of 32 up to 12288";
+        }
+    }
+    if (s.hidden % 16 != 0 || s.vocab <= 0 || s.vocab % 16 != 0 || s.vocab > 0x7fffffffLL) {
+        return "row counts must be multiples of 16";
+    }
+    if (s.max_seq <= 0 || s.max_pos <= 0) {
+        return "bad max_seq / max_pos";
+    }
+    return nullptr;
+}
+
+int num_ctas() {
+    return num_sms();
+}
+
+}  // namespace
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" size_t acb_lm_decode_scratch_bytes(const acb_decode_step * step) {
+    if (!step) {
+        return 0;
+    }
+    if (const char * why = check_shape(*step)) {
+        set_last_error(std::string("acb_lm_decode: ") + why);
+        return 0;
+    }
+    return scratch_map(*step, num_ctas()).total;
+}
+
+extern "C" acb_status acb_lm_decode_step(const acb_decode_step * step, acb_stream_t stream) {
+    if (!step || !step->layers || !step->embed || !step->head || !step->final_norm || !step->rope || !step->ids ||
+        !step->pos || !step->logits || !step->scratch) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (const char * why = check_shape(*step)) {
+        set_last_error(std::string("acb_lm_decode: ") + why);
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (step->greedy && step->hist && !step->hist_base) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if ((reinterpret_cast<uintptr_t>(step->head) & 15) || (reinterpret_cast<uintptr_t>(step->scratch) & 255)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    static int max_optin = 0;
+    if (max_optin == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    }
+    PdParams P{};
+    P.s       = *step;
+    P.n_ctas  = num_ctas();
+    P.n_split = std::min(kPdMaxSplit, std::max(1, P.n_ctas / step->n_kv_heads));
+    P.slots   = std::min(kPdMaxSlots, (max_optin - kSmRing) / kPdSlot);
+    if (P.slots < 4) {
+        set_last_error("acb_lm_decode: not enough shared memory for the weight ring");
+        return ACB_ERR_UNSUPPORTED;
+    }
+    P.bs_h = blocks_per_stage(step->hidden);
+    P.bs_q = blocks_per_stage(step->n_heads * kPdD);
+    P.bs_f = blocks_per_stage(step->ffn);
+    {
+        // prefetch distance: about one layer of this CTA's weights (ACB_PD_PREFETCH_KB overrides)
+        const char * env = std::getenv("ACB_PD_PREFETCH_KB");
+        P.prefetch       = env ? (int64_t) std::atoi(env) * 1024 : (int64_t) 384 * 1024;
+    }
+    const ScratchMap m = scratch_map(*step, P.n_ctas);
+    uint8_t *        sc = static_cast<uint8_t *>(step->scratch);
+    P.bar     = reinterpret_cast<unsigned *>(sc);
+    P.done    = reinterpret_cast<int *>(sc + 4);
+    P.tickets = reinterpret_cast<int *>(sc + 16);
+    P.hidden  = reinterpret_cast<float *>(sc + m.hidden);
+    P.qkv     = reinterpret_cast<float *>(sc + m.qkv);
+    P.scores  = reinterpret_cast<float *>(sc + m.scores);
+    P.smax    = reinterpret_cast<float *>(sc + m.smax);
+    P.part    = reinterpret_cast<float *>(sc + m.part);
+    P.att     = reinterpret_cast<float *>(sc + m.att);
+    P.gu      = reinterpret_cast<float *>(sc + m.gu);
+    P.bpart   = reinterpret_cast<float4 *>(sc + m.bpart);
+
+    const int  G     = step->n_heads / step->n_kv_heads;
+    const int  smem  = kSmRing + P.slots * kPdSlot;
+    void *     kern  = G == 1 ? (void *) lm_decode_kernel<1> : (G == 2 ? (void *) lm_decode_kernel<2> : (void *) lm_decode_kernel<4>);
+    cudaError_t e    = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    int         occ  = 0;
+    if (e == cudaSuccess) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kPdThreads, (size_t) smem);
+    }
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    if (occ < 1) {
+        set_last_error("acb_lm_decode: one CTA per SM does not fit");
+        return ACB_ERR_UNSUPPORTED;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) P.n_ctas);
+    cfg.blockDim           = dim3(kPdThreads);
+    cfg.dynamicSmemBytes   = (size_t) smem;
+    cfg.stream             = (cudaStream_t) stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id              = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs               = attr;
+    cfg.numAttrs            = 1;
+    void * args[]           = { &P };
+    e                       = cudaLaunchKernelExC(&cfg, kern, args);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}

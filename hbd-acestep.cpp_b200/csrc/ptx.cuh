@@ -76,6 +76,12 @@ __device__ __forceinline__ void bulk_g2s_stream(void * dst, const void * src, ui
         : "memory");
 }
 
+// Prefetch [src, src + bytes) into L2 (TMA engine; no shared-memory destination). src
+// 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void * src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

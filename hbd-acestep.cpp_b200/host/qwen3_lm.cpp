@@ -64,6 +64,10 @@ struct acb_qw3lm {
     int32_t *                           h_ids = nullptr;
     int32_t *                           h_pos = nullptr;
     std::map<long long, cudaGraphExec_t> graphs;
+    // single-sequence decode as one persistent launch (acb_lm_decode_step), when the shape allows
+    bool            persist = false;
+    DevBuf          pd_layers, pd_scratch;
+    acb_decode_step pd{};
 
     ~acb_qw3lm() {
         cudaSetDevice(device);
@@ -160,6 +164,9 @@ acb_status check_err(acb_qw3lm * m) {
     }
     if (e != 0) {
         cudaMemset(m->err.p, 0, sizeof(int));
+        if (m->persist) {
+            cudaMemset(m->pd_scratch.p, 0, m->pd_scratch.bytes);  // counters of an aborted step
+        }
         set_last_error("device error flag " + std::to_string(e));
         return ACB_ERR_DEVICE;
     }
@@ -182,6 +189,86 @@ const DevTensor * head_for(acb_qw3lm * m, int lm_offset, int lm_count, int * out
     }
     *out_v = m->c.vocab_size;
     return m->head_tiles_t.valid() ? &m->head_tiles_t : m->embed;
+}
+
+// The persistent single-sequence step needs every linear in tensor-core tiles with fused qkv and
+// gate|up rows, a Q8_0 embedding and its tiled head copy; otherwise the per-op graph runs.
+// ACB_LM_PERSIST=0 keeps the per-op graph (for comparisons).
+void setup_persistent(acb_qw3lm * m) {
+    const char * env = std::getenv("ACB_LM_PERSIST");
+    if (env && std::strcmp(env, "0") == 0) {
+        return;
+    }
+    const acb_qw3lm_config & c = m->c;
+    if (!m->head_tiles_t.valid() || m->embed->type != ACB_TYPE_Q8_0) {
+        return;
+    }
+    std::vector<acb_decode_layer> ls(c.n_layers);
+    for (int l = 0; l < c.n_layers; l++) {
+        const LMLayer & L = m->layers[l];
+        for (const DevTensor * t : { L.qkv, L.o, L.gate_up, L.down }) {
+            if (!t || t->type != ACB_TYPE_Q8_0_TILES || (reinterpret_cast<uintptr_t>(t->data) & 15)) {
+                return;
+            }
+        }
+        acb_decode_layer & d = ls[l];
+        d.qkv                = L.qkv->data;
+        d.o                  = L.o->data;
+        d.gate_up            = L.gate_up->data;
+        d.down               = L.down->data;
+        d.attn_norm          = (const float *) L.attn_norm->data;
+        d.post_norm          = (const float *) L.post_norm->data;
+        d.q_norm             = L.q_norm ? (const float *) L.q_norm->data : nullptr;
+        d.k_norm             = L.k_norm ? (const float *) L.k_norm->data : nullptr;
+        d.k_cache            = m->kc.as<uint16_t>() + (size_t) l * m->layer_elems;
+        d.v_cache            = m->vc.as<uint16_t>() + (size_t) l * m->layer_elems;
+    }
+    acb_decode_step & p = m->pd;
+    p.n_layers          = c.n_layers;
+    p.hidden            = c.hidden_size;
+    p.ffn               = c.intermediate_size;
+    p.n_heads           = c.n_heads;
+    p.n_kv_heads        = c.n_kv_heads;
+    p.head_dim          = c.head_dim;
+    p.eps               = c.rms_norm_eps;
+    p.attn_scale        = 1.0f / sqrtf((float) c.head_dim);
+    p.max_seq           = c.max_seq_len;
+    p.max_pos           = c.max_seq_len;
+    p.embed             = m->embed->data;
+    p.embed_rows        = m->embed->N;
+    p.head              = m->head_tiles_t.data;
+    p.vocab             = m->head_tiles_t.N;
+    p.final_norm        = (const float *) m->final_norm->data;
+    p.rope              = m->rope.as<float>();
+    p.ids               = m->ids.as<int32_t>();
+    p.pos               = m->pos.as<int32_t>();
+    p.logits            = m->logits.as<float>();
+    p.err               = m->err.as<int>();
+    const size_t sb     = acb_lm_decode_scratch_bytes(&p);
+    if (sb == 0 || m->pd_layers.alloc(ls.size() * sizeof(acb_decode_layer), false) != ACB_OK ||
+        m->pd_scratch.alloc(sb) != ACB_OK) {
+        return;
+    }
+    if (cudaMemcpy(m->pd_layers.p, ls.data(), ls.size() * sizeof(acb_decode_layer), cudaMemcpyHostToDevice) !=
+        cudaSuccess) {
+        return;
+    }
+    p.layers   = m->pd_layers.as<acb_decode_layer>();
+    p.scratch  = m->pd_scratch.p;
+    m->persist = true;
+}
+
+// One persistent step for kv set `set` (ids/pos already on the device).
+acb_status persistent_step(acb_qw3lm * m, int set, bool greedy) {
+    acb_decode_step p = m->pd;
+    p.kv_set          = set;
+    p.greedy          = greedy ? 1 : 0;
+    if (greedy) {
+        p.hist      = m->hist.as<int32_t>();
+        p.mhist     = m->mhist.as<float>();
+        p.hist_base = m->hist_base.as<int32_t>();
+    }
+    return acb_lm_decode_step(&p, (acb_stream_t) m->st);
 }
 
 // step graph: [embed gather] [layers] [head] (+ argmax/advance when greedy)
@@ -429,6 +516,7 @@ extern "C" acb_status acb_qw3lm_load(const char * gguf_path, int max_seq_len, in
     if (f) {
         return bad(ACB_ERR_OOM, "scratch allocation failed");
     }
+    setup_persistent(m);
     *out = m;
     return ACB_OK;
 }
@@ -447,6 +535,10 @@ extern "C" size_t acb_qw3lm_weight_bytes(const acb_qw3lm * m) {
 
 extern "C" int acb_qw3lm_kv_pos(const acb_qw3lm * m, int kv_set) {
     return (m && kv_set >= 0 && kv_set < m->n_sets) ? m->kv_pos[kv_set] : -1;
+}
+
+extern "C" int acb_qw3lm_persistent_decode(const acb_qw3lm * m) {
+    return m && m->persist ? 1 : 0;
 }
 
 extern "C" void acb_qw3lm_reset_kv(acb_qw3lm * m, int kv_set) {
@@ -562,8 +654,15 @@ extern "C" acb_status acb_qw3lm_forward_batch(acb_qw3lm * m, const int32_t * tok
         m->h_ids[i] = token_ids[i];
         m->h_pos[i] = m->kv_pos[set0 + i];
     }
-    const long long key = ((long long) N << 40) | ((long long) set0 << 32) | ((long long) (head == m->embed ? 0 : 1) << 31);
-    ACB_TRY(run_graph(m, key, N, set0, head, out_v, false, true));
+    if (N == 1 && m->persist && head == &m->head_tiles_t) {
+        cudaMemcpyAsync(m->ids.p, m->h_ids, sizeof(int32_t), cudaMemcpyHostToDevice, m->st);
+        cudaMemcpyAsync(m->pos.p, m->h_pos, sizeof(int32_t), cudaMemcpyHostToDevice, m->st);
+        ACB_TRY(persistent_step(m, set0, false));
+    } else {
+        const long long key =
+            ((long long) N << 40) | ((long long) set0 << 32) | ((long long) (head == m->embed ? 0 : 1) << 31);
+        ACB_TRY(run_graph(m, key, N, set0, head, out_v, false, true));
+    }
     cudaMemcpyAsync(logits, m->logits.p, sizeof(float) * (size_t) N * out_v, cudaMemcpyDeviceToHost, m->st);
     ACB_TRY(sync(m));
     for (int i = 0; i < N; i++) {
@@ -603,8 +702,11 @@ extern "C" acb_status acb_qw3lm_generate_greedy(acb_qw3lm * m, const int32_t * l
     cudaEventCreate(&e1);
     cudaEventRecord(e0, m->st);
     acb_status s = ACB_OK;
+    int               hv    = 0;
+    const DevTensor * ghead = head_for(m, 0, 0, &hv);
+    const bool        pers  = N == 1 && m->persist;
     for (int k = 0; k < n_steps && s == ACB_OK; k++) {
-        s = run_graph(m, key, N, set0, m->embed, m->c.vocab_size, true, false);
+        s = pers ? persistent_step(m, set0, true) : run_graph(m, key, N, set0, ghead, hv, true, false);
     }
     cudaEventRecord(e1, m->st);
     if (s == ACB_OK) {

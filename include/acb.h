@@ -455,6 +455,61 @@ ACB_API acb_status acb_argmax_noalloc(const float * logits, int64_t stride, int6
                                       float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
                                       int64_t hist_stride, const int32_t * hist_base, int flags, acb_stream_t stream);
 
+/* ---- whole batch-1 decode step in one persistent launch ------------------------------------
+ * One Qwen3 LM decode step for one sequence (qw3lm_forward_batch with N = 1,
+ * src/qwen3-lm.h:557-823, and the temperature-0 sampler, src/sampling.h:30-34) as a single
+ * cooperative kernel with one CTA per SM: token gather, every layer (RMSNorm -> QKV GEMV ->
+ * q/k-norm + RoPE + f16 cache write -> f16-cache attention -> o GEMV + residual -> RMSNorm ->
+ * gate|up GEMV -> SwiGLU -> down GEMV + residual), final RMSNorm, the head GEMV and the argmax.
+ * Each CTA's weight bytes stream through its shared-memory ring without a break across layers;
+ * stages that need the whole previous vector wait at a bounded grid-wide barrier. Arithmetic per
+ * op is that of the separate kernels (acb_gemv on ACB_TYPE_Q8_0_TILES, acb_qkv_post,
+ * acb_attn_decode, acb_argmax). */
+typedef struct acb_decode_layer {
+    const void *  qkv;       /* Q8_0_TILES [Nh*D + 2*Nkv*D][H]: q rows, k rows, v rows */
+    const void *  o;         /* Q8_0_TILES [H][Nh*D] */
+    const void *  gate_up;   /* Q8_0_TILES [2F][H]: gate rows, then up rows */
+    const void *  down;      /* Q8_0_TILES [H][F] */
+    const float * attn_norm; /* [H] */
+    const float * post_norm; /* [H] */
+    const float * q_norm;    /* [D] or NULL */
+    const float * k_norm;    /* [D] or NULL */
+    uint16_t *    k_cache;   /* f16 [n_sets][Nkv][max_seq][D] of this layer */
+    uint16_t *    v_cache;
+} acb_decode_layer;
+
+typedef struct acb_decode_step {
+    const acb_decode_layer * layers; /* device array [n_layers] */
+    int           n_layers, hidden, ffn, n_heads, n_kv_heads, head_dim; /* head_dim 128; Nh/Nkv in {1,2,4} */
+    float         eps, attn_scale;
+    int           max_seq, max_pos, kv_set;
+    const void *  embed;      /* Q8_0 GGUF rows [embed_rows][H] (token gather) */
+    int64_t       embed_rows;
+    const void *  head;       /* Q8_0_TILES [vocab][H] */
+    int64_t       vocab;      /* multiple of 16 */
+    const float * final_norm; /* [H] */
+    const float * rope;       /* [max_pos][D]: (cos, sin) of pair i at 2i, 2i+1 */
+    int32_t *     ids;        /* [1] token of this step; the next token when greedy */
+    int32_t *     pos;        /* [1] kv position of this step; += 1 when greedy */
+    float *       logits;     /* [vocab] */
+    int           greedy;     /* 1: argmax -> ids[0], margin, history, pos[0] += 1 */
+    float *       margin;     /* [1] top1 - top2, or NULL */
+    int32_t *     hist;       /* token history [max_seq] at pos - hist_base[0], or NULL */
+    float *       mhist;      /* margin history, or NULL */
+    const int32_t * hist_base;
+    void *        scratch;    /* acb_lm_decode_scratch_bytes, zeroed before first use; every
+                                 successful step leaves its counters at zero */
+    int *         err;        /* ACB_DEVERR_* bits */
+} acb_decode_step;
+
+/* Device scratch the step needs (0 when the shape is unsupported: see acb_last_error). */
+ACB_API size_t acb_lm_decode_scratch_bytes(const acb_decode_step * step);
+/* Enqueue one step. ACB_ERR_UNSUPPORTED for shapes outside the kernel (head_dim != 128,
+ * Nh/Nkv not in {1,2,4}, a width above 12288 or not a multiple of 32, N not a multiple of 16)
+ * or a device that cannot hold one CTA per SM; the caller keeps its per-op path for those.
+ * After a step that raised a device error the scratch must be zeroed again. */
+ACB_API acb_status acb_lm_decode_step(const acb_decode_step * step, acb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

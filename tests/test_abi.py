@@ -54,3 +54,33 @@ def test_rope_table_matches_oracle_bitexact():
         t = acb.rope_table(n, D, base).numpy()
         ref = O.rope_cache(np.arange(n, dtype=np.int32), D, base)
         assert np.array_equal(t.view(np.uint32), ref.view(np.uint32))
+
+
+class _DecodeStep(C.Structure):
+    """acb_decode_step (acb.h), for argument checks only."""
+    _fields_ = [("layers", C.c_void_p), ("n_layers", C.c_int), ("hidden", C.c_int), ("ffn", C.c_int),
+                ("n_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("eps", C.c_float),
+                ("attn_scale", C.c_float), ("max_seq", C.c_int), ("max_pos", C.c_int), ("kv_set", C.c_int),
+                ("embed", C.c_void_p), ("embed_rows", C.c_int64), ("head", C.c_void_p), ("vocab", C.c_int64),
+                ("final_norm", C.c_void_p), ("rope", C.c_void_p), ("ids", C.c_void_p), ("pos", C.c_void_p),
+                ("logits", C.c_void_p), ("greedy", C.c_int), ("margin", C.c_void_p), ("hist", C.c_void_p),
+                ("mhist", C.c_void_p), ("hist_base", C.c_void_p), ("scratch", C.c_void_p), ("err", C.c_void_p)]
+
+
+def test_persistent_decode_shape_checks():
+    L = acb.lib()
+    L.acb_lm_decode_scratch_bytes.restype = C.c_size_t
+    assert L.acb_lm_decode_step(None, None) == 1
+    assert L.acb_lm_decode_scratch_bytes(None) == 0
+    s = _DecodeStep(n_layers=28, hidden=2048, ffn=6144, n_heads=16, n_kv_heads=8, head_dim=128, eps=1e-6,
+                    attn_scale=0.088, max_seq=8192, max_pos=8192, vocab=217472, embed_rows=217472)
+    n = L.acb_lm_decode_scratch_bytes(C.byref(s))
+    # scores [16][8192] f32 dominate; every region is present
+    assert 16 * 8192 * 4 < n < 16 * 8192 * 4 + 4 * 1024 * 1024
+    for field, bad in [("head_dim", 64), ("n_kv_heads", 2), ("ffn", 6000), ("vocab", 217473), ("hidden", 16384)]:
+        t = _DecodeStep.from_buffer_copy(s)
+        setattr(t, field, bad)
+        assert L.acb_lm_decode_scratch_bytes(C.byref(t)) == 0, field
+        assert "acb_lm_decode" in L.acb_last_error().decode()
+    # every pointer null: invalid before any shape or device check
+    assert L.acb_lm_decode_step(C.byref(s), None) == 1

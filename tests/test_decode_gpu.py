@@ -280,3 +280,77 @@ def test_gemv_q8_0_tiles(cuda, M, N, K):
     y = acb.gemv(Wt, acb.Q8_0_TILES, N, K, T(gu, cuda), M=M, prologue=acb.PRO_SWIGLU, x_stride=2 * K)
     ref = O.mul_mat(O.Q8_0, W, N, K, O.swiglu(gu[:, :K], gu[:, K:]))
     assert max_rel(y.cpu().numpy(), ref) <= 5e-4 and cos_sim(y.cpu().numpy(), ref) > 0.999999
+
+
+# ---- single-sequence decode as one persistent launch (acb_lm_decode_step) ----------------------
+
+def _persist_pair(tmp_path, cfg, seed, max_seq=512):
+    """One GGUF loaded twice: persistent single-sequence decode, and the per-op graph."""
+    import os
+    p = str(tmp_path / "lm16.gguf")
+    t = make_tensors(cfg, policy_all(O.Q8_0), seed=seed, embed_std=0.5)
+    write_gguf(p, cfg, t)
+    a = acb.QW3LM(p, max_seq_len=max_seq, n_kv_sets=2)
+    os.environ["ACB_LM_PERSIST"] = "0"
+    try:
+        b = acb.QW3LM(p, max_seq_len=max_seq, n_kv_sets=2)
+    finally:
+        del os.environ["ACB_LM_PERSIST"]
+    return a, b, t
+
+
+# vocabulary a multiple of 16 (the head is tiled); q heads per kv head 2, 4, 1; one wide layer
+# (ffn 6144: three activation chunks per thread in the down projection's prologue)
+PERSIST_CFGS = {
+    "g2": dict(TINY, vocab_size=1008),
+    "g4": dict(TINY, vocab_size=1008, num_key_value_heads=1),
+    "g1": dict(TINY, vocab_size=1008, num_key_value_heads=4),
+    "wide": dict(TINY, vocab_size=2048, hidden_size=2048, intermediate_size=6144, num_hidden_layers=1,
+                 num_attention_heads=16, num_key_value_heads=8),
+}
+
+
+@pytest.mark.parametrize("name", list(PERSIST_CFGS))
+def test_lm_persistent_greedy(cuda, tmp_path, name):
+    cfg = PERSIST_CFGS[name]
+    per, ref, t = _persist_pair(tmp_path, cfg, seed=31)
+    assert per.persistent_decode() and not ref.persistent_decode()
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, cfg["vocab_size"], size=150).astype(np.int32)
+    lg = per.forward(prompt, kv_set=0)
+    ref.forward(prompt, kv_set=0)
+    n = 24
+    first = int(np.argmax(lg))
+    toks, marg, _ = per.generate_greedy([first], 0, n, want_margins=True)
+    rtoks, rmarg, _ = ref.generate_greedy([first], 0, n, want_margins=True)
+    assert toks[0].tolist() == rtoks[0].tolist(), (toks, rtoks)
+    assert np.allclose(marg, rmarg, rtol=1e-3, atol=1e-4)
+    ora = oracle_model(cfg, t)
+    ora.alloc_kv(1, 512)
+    otoks, omarg = oracle_greedy(ora, prompt, n)
+    assert toks[0].tolist() == otoks, (toks[0].tolist(), otoks, omarg)
+    assert per.kv_pos(0) == 150 + n
+    per.close()
+    ref.close()
+
+
+def test_lm_persistent_forward_batch(cuda, tmp_path):
+    cfg = PERSIST_CFGS["g2"]
+    per, ref, t = _persist_pair(tmp_path, cfg, seed=32)
+    ora = oracle_model(cfg, t)
+    ora.alloc_kv(2, 512)
+    rng = np.random.default_rng(4)
+    p = rng.integers(0, cfg["vocab_size"], size=77).astype(np.int32)
+    per.forward(p, kv_set=1)
+    ref.forward(p, kv_set=1)
+    ora.prefill(p, set_=1)
+    for step in range(4):
+        ids = rng.integers(0, cfg["vocab_size"], size=1).astype(np.int32)
+        g = per.forward_batch(ids, [1])
+        h = ref.forward_batch(ids, [1])
+        r = ora.decode(ids, set0=1)
+        assert cos_sim(g[0], r[0]) > 0.99999 and max_rel(g[0], r[0]) < 1e-3, (step, cos_sim(g[0], r[0]))
+        assert cos_sim(g[0], h[0]) > 0.999999 and max_rel(g[0], h[0]) < 1e-4, (step, max_rel(g[0], h[0]))
+    assert per.kv_pos(1) == 81 and per.kv_pos(0) == 0
+    per.close()
+    ref.close()
