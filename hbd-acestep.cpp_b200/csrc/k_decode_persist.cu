@@ -10,7 +10,7 @@
 //     35 KB shared-memory slots with 1-D bulk copies. Weights do not depend on activations, so
 //     the stream never waits for a layer boundary, only for a free slot;
 //   - warps 0-7 are consumers: before each GEMV they build the quantised activation in shared
-//     memory (RMSNorm * w, SwiGLU or the attention output, then Q8_0 blocks), then run a dp4a
+//     memory (RMSNorm * w, the SwiGLU vector or the attention output, then Q8_0 blocks), then run a dp4a
 //     GEMV over their range of Q8_0 tiles (ACB_TYPE_Q8_0_TILES): one activation column makes
 //     the int8 MMA of k_gemv.cu a poor fit, and eight independent blocks per warp and stage
 //     keep the shared-memory ring draining at HBM rate;
@@ -56,7 +56,6 @@ constexpr int      kPdSlot        = kPdStageBlocks * kPdTileBlk;  // 34816 bytes
 constexpr int      kPdMaxSlots    = 16;
 constexpr int      kPdBpw         = kPdStageBlocks / kPdWarps;  // blocks per warp per stage
 constexpr int      kPdMaxK        = 12288;
-constexpr int      kPdMaxChunks   = kPdMaxK / 4 / kPdCons;  // float4 activation chunks per thread
 constexpr int      kPdMaxSplit    = 32;
 constexpr int      kPdD           = 128;
 constexpr unsigned kAbortBit      = 0x80000000u;
@@ -67,7 +66,8 @@ constexpr int kSmFull   = 0;     // uint64 full[16]
 constexpr int kSmEmpty  = 128;   // uint64 empty[16]
 constexpr int kSmRed    = 256;   // double [16][4]
 constexpr int kSmMisc   = 768;   // float inv[4], int flags
-constexpr int kSmTred   = 1024;  // float [2][16 warps][16 rows]
+constexpr int kSmTred   = 1024;  // float [2][8 warps][16 rows]
+constexpr int kSmGate   = 2048;  // float [256] gate rows of this CTA's SwiGLU tiles; residual rows
 constexpr int kSmAct    = 3072;  // int8 xq[kPdMaxK] + float xd[kPdMaxK/32]; attention scratch
 constexpr int kSmRing   = (kSmAct + kPdMaxK + kPdMaxK / 32 * 4 + 127) / 128 * 128;
 // attention scratch inside the activation region
@@ -87,6 +87,7 @@ __device__ __forceinline__ volatile int * sm_abort() { return reinterpret_cast<v
 __device__ __forceinline__ volatile int * sm_last() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 36); }
 __device__ __forceinline__ float * sm_tred() { return reinterpret_cast<float *>(pd_smem + kSmTred); }
 __device__ __forceinline__ uint8_t * sm_act() { return pd_smem + kSmAct; }
+__device__ __forceinline__ float * sm_gate() { return reinterpret_cast<float *>(pd_smem + kSmGate); }
 __device__ __forceinline__ int8_t * sm_xq() { return reinterpret_cast<int8_t *>(pd_smem + kSmAct); }
 __device__ __forceinline__ float * sm_xd() { return reinterpret_cast<float *>(pd_smem + kSmAct + kPdMaxK); }
 __device__ __forceinline__ uint8_t * sm_ring() { return pd_smem + kSmRing; }
@@ -102,7 +103,7 @@ struct PdParams {
     float *         smax;    // [Nh][kPdMaxSplit]
     float *         part;    // [kPdMaxSplit][Nh][D]
     float *         att;     // [Nh*D]
-    float *         gu;      // [2F]
+    float *         gu;      // [F] silu(gate) * up
     float4 *        bpart;   // [n_ctas]
     unsigned *      bar;
     int *           done;
@@ -167,51 +168,62 @@ __device__ __forceinline__ void pd_range(int64_t n_tiles, int gi, int c, int G, 
 }
 
 // ---- producer: the CTA's whole weight stream of the step -----------------------------------
-// Byte range of this CTA's tiles of GEMV k of the step (k = 4 l + {qkv, o, gate|up, down};
-// k = 4 n_layers is the head); tiles of a range are contiguous, blocks in K order.
+// Byte range of this CTA's tiles of stream segment k of the step: per layer l, segments 5 l +
+// {qkv, o, gate rows, up rows, down}; 5 n_layers is the head. Tiles of a range are contiguous,
+// blocks in K order. The gate and up pieces of the gate|up weight take the same tile range (a
+// CTA owns whole rows of the SwiGLU). gi is the GEMV index that rotates the assignment.
 __device__ void pd_segment(const PdParams & P, int k, const uint8_t *& ptr, int64_t & bytes, int & K, int & bs) {
     const acb_decode_step & S  = P.s;
     const int               qd = S.n_heads * S.head_dim;
     const uint8_t *         W;
-    int64_t                 n_rows;
-    if (k == 4 * S.n_layers) {
+    int64_t                 n_rows, row0 = 0;
+    int                     gi;
+    if (k == 5 * S.n_layers) {
         W      = (const uint8_t *) S.head;
         n_rows = S.vocab;
         K      = S.hidden;
         bs     = P.bs_h;
+        gi     = 4 * S.n_layers;
     } else {
-        const acb_decode_layer & L = S.layers[k >> 2];
-        switch (k & 3) {
+        const int                l = k / 5;
+        const acb_decode_layer & L = S.layers[l];
+        switch (k - 5 * l) {
             case 0:
                 W      = (const uint8_t *) L.qkv;
                 n_rows = qd + 2 * S.n_kv_heads * S.head_dim;
                 K      = S.hidden;
                 bs     = P.bs_h;
+                gi     = 4 * l;
                 break;
             case 1:
                 W      = (const uint8_t *) L.o;
                 n_rows = S.hidden;
                 K      = qd;
                 bs     = P.bs_q;
+                gi     = 4 * l + 1;
                 break;
             case 2:
+            case 3:
                 W      = (const uint8_t *) L.gate_up;
-                n_rows = 2 * (int64_t) S.ffn;
+                n_rows = S.ffn;
+                row0   = (k - 5 * l == 3) ? S.ffn : 0;
                 K      = S.hidden;
                 bs     = P.bs_h;
+                gi     = 4 * l + 2;
                 break;
             default:
                 W      = (const uint8_t *) L.down;
                 n_rows = S.hidden;
                 K      = S.ffn;
                 bs     = P.bs_f;
+                gi     = 4 * l + 3;
                 break;
         }
     }
     int64_t t0, t1;
-    pd_range(n_rows / 16, k, blockIdx.x, P.n_ctas, t0, t1);
+    pd_range(n_rows / 16, gi, blockIdx.x, P.n_ctas, t0, t1);
     const int64_t tile_bytes = (int64_t) (K / 32) * kPdTileBlk;
-    ptr                      = W + t0 * tile_bytes;
+    ptr                      = W + (row0 / 16 + t0) * tile_bytes;
     bytes                    = (t1 - t0) * tile_bytes;
 }
 
@@ -225,7 +237,7 @@ __device__ void pd_producer(const PdParams & P) {
     volatile int * s_abort = sm_abort();
     const acb_decode_step & S     = P.s;
     const uint64_t          pol   = ptx::policy_evict_first();
-    const int               nseg  = 4 * S.n_layers + 1;
+    const int               nseg  = 5 * S.n_layers + 1;
     uint32_t                it    = 0;
     bool                    ok    = true;
     // prefetch cursor
@@ -350,21 +362,22 @@ __device__ __forceinline__ bool pd_wait_full(const PdParams & P, PdCtx & x, int 
     return false;
 }
 
-enum { ACT_X = 0, ACT_RMS = 1, ACT_SWIGLU = 2, ACT_EMBED = 3 };
+enum { ACT_X = 0, ACT_RMS = 1, ACT_EMBED = 3 };
 
 // Activation of K elements -> Q8_0 blocks in shared memory (quantize_q8_0 arithmetic). Thread t
 // owns float4 chunks t, t + 512, ...; the 8 chunks of a 32-element block sit in 8 adjacent lanes.
 // All loads (activation and norm gains) are issued before the first use.
+// Chunks c0 .. c0 + NCH - 1 of every thread; the RMSNorm modes take all chunks in one call.
 template <int MODE, int NCH>
 __device__ void pd_act_quant_n(const PdParams & P, PdCtx & x, const float * src, const float * w,
-                               const uint8_t * erow, int K, float * raw_out) {
+                               const uint8_t * erow, int K, float * raw_out, int c0 = 0, bool last = true) {
     const int tid = threadIdx.x, lane = tid & 31;
     const int nf  = K / 4;
     float4    v[NCH], ww[NCH];
 #pragma unroll
     for (int i = 0; i < NCH; i++) {
         // loads at a clamped index, then a select (predicated loads cost registers)
-        const int f  = tid + i * kPdCons;
+        const int f  = tid + (c0 + i) * kPdCons;
         const int fc = min(f, nf - 1);
         ww[i]        = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
         if ((MODE == ACT_RMS || MODE == ACT_EMBED) && w) {
@@ -381,11 +394,6 @@ __device__ void pd_act_quant_n(const PdParams & P, PdCtx & x, const float * src,
                 if (raw_out) {
                     reinterpret_cast<float4 *>(raw_out)[f] = v[i];
                 }
-            } else if (MODE == ACT_SWIGLU) {
-                const float4 g = __ldcg(reinterpret_cast<const float4 *>(src) + f);
-                const float4 u = __ldcg(reinterpret_cast<const float4 *>(src + K) + f);
-                v[i] = make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z),
-                                   silu_times(g.w, u.w));
             } else {
                 v[i] = __ldcg(reinterpret_cast<const float4 *>(src) + f);
             }
@@ -429,10 +437,10 @@ __device__ void pd_act_quant_n(const PdParams & P, PdCtx & x, const float * src,
     }
 #pragma unroll
     for (int i = 0; i < NCH; i++) {
-        if (i * kPdCons >= nf) {
+        if ((c0 + i) * kPdCons >= nf) {
             break;  // uniform over the CTA
         }
-        const int f    = tid + i * kPdCons;
+        const int f    = tid + (c0 + i) * kPdCons;
         float     amax = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
         amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
         amax           = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
@@ -455,7 +463,9 @@ __device__ void pd_act_quant_n(const PdParams & P, PdCtx & x, const float * src,
             }
         }
     }
-    cons_sync();
+    if (last) {
+        cons_sync();
+    }
 }
 
 template <int MODE>
@@ -465,12 +475,18 @@ __device__ __forceinline__ void pd_act_quant(const PdParams & P, PdCtx & x, cons
         pd_act_quant_n<MODE, 2>(P, x, src, w, erow, K, raw_out);
     } else if (K <= kPdCons * 16) {
         pd_act_quant_n<MODE, 4>(P, x, src, w, erow, K, raw_out);
+    } else if (K <= kPdCons * 24 || MODE != ACT_X) {
+        pd_act_quant_n<MODE, 6>(P, x, src, w, erow, K, raw_out);  // RMSNorm widths are at most 6144
     } else {
-        pd_act_quant_n<MODE, kPdMaxChunks>(P, x, src, w, erow, K, raw_out);
+        // wide plain activations in two batches of six chunks (one register set of the
+        // six-chunk form; a twelve-chunk form would spill)
+        pd_act_quant_n<MODE, 6>(P, x, src, w, erow, K, raw_out, 0, false);
+        pd_act_quant_n<MODE, 6>(P, x, src, w, erow, K, raw_out, 6, true);
     }
 }
 
-enum { EPI_STORE = 0, EPI_ADD = 1, EPI_HEAD = 2 };
+// EPI_GATE keeps the rows in shared memory; EPI_UP writes silu(gate) * up of the same rows
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_HEAD = 2, EPI_GATE = 3, EPI_UP = 4 };
 
 // One 16-row x 32-column tile block for one activation column. Lane 4g + q holds bytes
 // 4q..4q+3 and 16+4q..16+4q+3 of rows g and g + 8 (the tile order) and the activation words q
@@ -489,8 +505,19 @@ __device__ __forceinline__ void pd_block(const uint4 & a, uint32_t dw, uint2 xw,
 // Tensor-core Q8_0 tile GEMV over this CTA's tile range (gemv_tiles_kernel arithmetic for one
 // activation column): warp w takes blocks w, w + 16, ... of every stage; at the end of a tile
 // the 16 warps' partials are added in warp order by one warp (rotating) and stored.
+// Residual row of the reducer lane (lane < 16) of warp w for EPI_ADD GEMV gi: y[(t0 + w) * 16 +
+// lane]. Requested a whole stage ahead of the GEMV (the rows last changed two barriers earlier),
+// so the epilogue finds it in a register.
+__device__ __forceinline__ float pd_residual(const PdParams & P, int64_t n_rows, int gi, const float * y) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int64_t   t0, t1;
+    pd_range(n_rows / 16, gi, blockIdx.x, P.n_ctas, t0, t1);
+    return (lane < 16 && t0 + warp < t1) ? __ldcg(y + (t0 + warp) * 16 + lane) : 0.0f;
+}
+
 template <int EPI>
-__device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n_rows, int K, int bs, int gi, float * y, Best & best) {
+__device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n_rows, int K, int bs, int gi, float * y,
+                                        Best & best, float resv = 0.0f) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, q = lane & 3;
     int64_t   t0, t1;
@@ -578,7 +605,11 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
             }
             const int64_t row = t * 16 + lane;
             if (EPI == EPI_ADD) {
-                y[row] = __fadd_rn(__ldcg(y + row), v);
+                y[row] = __fadd_rn(t - t0 < kPdWarps ? resv : __ldcg(y + row), v);
+            } else if (EPI == EPI_GATE) {
+                sm_gate()[(t - t0) * 16 + lane] = v;
+            } else if (EPI == EPI_UP) {
+                y[row] = silu_times(sm_gate()[(t - t0) * 16 + lane], v);
             } else {
                 y[row] = v;
             }
@@ -630,6 +661,26 @@ __device__ __forceinline__ void pd_norm_rope(const float * src, const float * w,
 // (kv head, split) and kPdMaxSplit. Both passes of a step derive the same value.
 __device__ __forceinline__ int pd_splits(const PdParams & P, int n) {
     return min(P.n_split, max(1, (n + 63) / 64));
+}
+
+// L2 prefetch of the K and V rows (positions before p) of this CTA's attention split, issued at
+// the start of the layer: the cache rows do not depend on the step, and fetching them from HBM
+// after the QKV barrier would put an HBM round trip on the critical path twice.
+template <int G>
+__device__ __forceinline__ void pd_kv_prefetch(const PdParams & P, const acb_decode_layer & L, int p) {
+    const acb_decode_step & S = P.s;
+    const int               kv_len = p + 1, ns = pd_splits(P, kv_len), c = blockIdx.x;
+    if (threadIdx.x != 0 || c >= S.n_kv_heads * ns) {
+        return;
+    }
+    const int     h = c / ns, sp = c % ns, chunk = (kv_len + ns - 1) / ns;
+    const int     j0 = sp * chunk, j1 = min(p, j0 + chunk);  // position p is written this step
+    const int64_t base = (((int64_t) S.kv_set * S.n_kv_heads + h) * S.max_seq + j0) * kPdD;
+    if (j1 > j0) {
+        const uint32_t bytes = (uint32_t) (j1 - j0) * kPdD * 2;
+        ptx::bulk_prefetch_l2(L.k_cache + base, bytes);
+        ptx::bulk_prefetch_l2(L.v_cache + base, bytes);
+    }
 }
 
 // Attention pass 1 for CTA (kv head h, split s): q heads of the group, the new k/v (by the
@@ -705,7 +756,7 @@ __device__ void pd_attn_scores(const PdParams & P, PdCtx & x, const acb_decode_l
             d[2 * lane + e]      = __half_as_ushort(__float2half_rn(v[e]));
             d[64 + 2 * lane + e] = __half_as_ushort(__float2half_rn(v[2 + e]));
         }
-        __threadfence();  // read back by pass 2 of this CTA through L2
+        // read back by pass 2 through L2 after the grid barrier, whose fence publishes it
     }
     cons_sync();
     float qv[G][16];
@@ -822,6 +873,17 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
     };
     int jb = j0 + wi;
     load_pv(jb);
+    // the first batch of the softmax-sum scores does not depend on the max either
+    constexpr int US = 8;
+    float         ts[G][US];
+#pragma unroll
+    for (int gg = 0; gg < G; gg++) {
+        const float * r = P.scores + (int64_t) (h * G + gg) * S.max_seq;
+#pragma unroll
+        for (int u = 0; u < US; u++) {
+            ts[gg][u] = __ldcg(r + min(tid + u * kPdCons, kv_len - 1));  // clamped: summed only if in range
+        }
+    }
     float * sM = sm_misc() + 4;
     if (warp < G) {
         float m = lane < ns ? __ldcg(P.smax + (int64_t) (h * G + warp) * kPdMaxSplit + lane) : -INFINITY;
@@ -836,8 +898,7 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
     for (int gg = 0; gg < G; gg++) {
         M[gg] = sM[gg];
     }
-    // sum of expf(s - M) in double over each whole row: thread t takes j = t + 512 i
-    constexpr int US = 8;
+    // sum of expf(s - M) in double over each whole row: thread t takes j = t + 256 i
 #pragma unroll
     for (int gg = 0; gg < G; gg++) {
         const float * r = P.scores + (int64_t) (h * G + gg) * S.max_seq;
@@ -846,7 +907,7 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
             float t[US];
 #pragma unroll
             for (int u = 0; u < US; u++) {
-                t[u] = j + u * kPdCons < kv_len ? __ldcg(r + j + u * kPdCons) : 0.0f;
+                t[u] = j == tid ? ts[gg][u] : __ldcg(r + min(j + u * kPdCons, kv_len - 1));
             }
 #pragma unroll
             for (int u = 0; u < US; u++) {
@@ -1008,10 +1069,12 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
         } else {
             pd_act_quant<ACT_RMS>(P, x, P.hidden, L.attn_norm, nullptr, S.hidden, nullptr);
         }
+        pd_kv_prefetch<G>(P, L, p);
         ok = pd_gemv<EPI_STORE>(P, x, qkvd, S.hidden, P.bs_h, 4 * l, P.qkv, best) && pd_grid_sync(P, x);
         if (!ok) {
             break;
         }
+        const float res_o = pd_residual(P, S.hidden, 4 * l + 1, P.hidden);
         pd_attn_scores<G>(P, x, L, p);
         if (!pd_grid_sync(P, x)) {
             break;
@@ -1021,18 +1084,19 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
             break;
         }
         pd_act_quant<ACT_X>(P, x, P.att, nullptr, nullptr, qd, nullptr);
-        ok = pd_gemv<EPI_ADD>(P, x, S.hidden, qd, P.bs_q, 4 * l + 1, P.hidden, best) && pd_grid_sync(P, x);
+        ok = pd_gemv<EPI_ADD>(P, x, S.hidden, qd, P.bs_q, 4 * l + 1, P.hidden, best, res_o) && pd_grid_sync(P, x);
         if (!ok) {
             break;
         }
+        const float res_d = pd_residual(P, S.hidden, 4 * l + 3, P.hidden);
         pd_act_quant<ACT_RMS>(P, x, P.hidden, L.post_norm, nullptr, S.hidden, nullptr);
-        ok = pd_gemv<EPI_STORE>(P, x, 2 * (int64_t) S.ffn, S.hidden, P.bs_h, 4 * l + 2, P.gu, best) &&
-             pd_grid_sync(P, x);
+        ok = pd_gemv<EPI_GATE>(P, x, S.ffn, S.hidden, P.bs_h, 4 * l + 2, nullptr, best) &&
+             pd_gemv<EPI_UP>(P, x, S.ffn, S.hidden, P.bs_h, 4 * l + 2, P.gu, best) && pd_grid_sync(P, x);
         if (!ok) {
             break;
         }
-        pd_act_quant<ACT_SWIGLU>(P, x, P.gu, nullptr, nullptr, S.ffn, nullptr);
-        ok = pd_gemv<EPI_ADD>(P, x, S.hidden, S.ffn, P.bs_f, 4 * l + 3, P.hidden, best) && pd_grid_sync(P, x);
+        pd_act_quant<ACT_X>(P, x, P.gu, nullptr, nullptr, S.ffn, nullptr);
+        ok = pd_gemv<EPI_ADD>(P, x, S.hidden, S.ffn, P.bs_f, 4 * l + 3, P.hidden, best, res_d) && pd_grid_sync(P, x);
     }
     if (!ok) {
         return;
@@ -1129,6 +1193,9 @@ const char * check_shape(const acb_decode_step & s) {
         if (k <= 0 || k % 32 != 0 || k > kPdMaxK) {
             return "hidden, ffn and Nh*D must be multiples of 32 up to 12288";
         }
+    }
+    if (s.hidden > kPdCons * 24) {
+        return "hidden must be at most 6144";
     }
     if (s.hidden % 16 != 0 || s.vocab <= 0 || s.vocab % 16 != 0 || s.vocab > 0x7fffffffLL) {
         return "row counts must be multiples of 16";
