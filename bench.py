@@ -332,6 +332,14 @@ def run_ours(args):
     acb.lib()
     stream = torch.cuda.current_stream()
 
+    if args.workloads == "lm5":
+        r = run_lm5(dev, rank, ws)
+        if rank == 0:
+            print(json.dumps(dict(r, data="synthetic", dtype="int8-dot/f32 (Q8_K-quantised activations)")),
+                  flush=True)
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return
     if args.workloads == "gemv":
         print(json.dumps(run_gemv_shapes(dev)), flush=True)
         return
@@ -387,6 +395,10 @@ def run_ours(args):
             if "enc" in wl:
                 torch.cuda.empty_cache()
                 line["text_encoder"] = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
+        if "lm5" in wl:
+            # config 5's LM shards one sequence per GPU: run at every N (all ranks take part)
+            torch.cuda.empty_cache()
+            line["lm5_decode"] = run_lm5(dev, rank, ws)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -787,6 +799,89 @@ def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None, prompt_len=L
     except OSError:
         pass
     return res
+
+
+# ---- workload: BASELINE config 5's LM (Qwen3-4B shape, Q4_K_M, one sequence per GPU) ------------
+
+LM5_PROMPT, LM5_GEN = 1024, 2048
+
+
+def run_lm5(dev, rank, ws, prompt_len=LM5_PROMPT, gen_len=LM5_GEN, warm_tokens=16):
+    """Config 5's LM on every rank: the Qwen3-4B shape quantised with the Q4_K_M policy of
+    tools/quantize.cpp (Q4_K base, v/down bumped to Q6_K in the listed layers, Q6_K embedding =
+    tied head), a 1024-token random prompt and 2048 greedy tokens per sequence, one independent
+    sequence per GPU (weak scaling, no exchange during decode). The ranks' token streams are
+    gathered over NCCL at the end. Time: the library's CUDA events around the device greedy loop,
+    max over ranks; value = all ranks' tokens / that time."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+    import synthetic
+
+    cfg = dict(synthetic.QWEN3_4B)
+    V = cfg["vocab_size"]
+    path = os.path.join(tempfile.gettempdir(), "acb_bench_lm4b_q4_k_m.gguf")
+    t0 = time.time()
+    if rank == 0:
+        synthetic.write_lm_gguf(path, cfg, synthetic.policy_q4_k_m, seed=45, device=str(dev))
+    if ws > 1:
+        torch.distributed.barrier()
+    t_gen = time.time() - t0
+    m = acb.QW3LM(path, max_seq_len=prompt_len + gen_len + 64, n_kv_sets=1, device=dev.index or 0)
+    wb = m.weight_bytes()
+    rng = np.random.default_rng(70 + rank)
+    prompt = rng.integers(0, V, size=prompt_len).astype(np.int32)
+    t0 = time.time()
+    lg = m.forward(prompt, kv_set=0)
+    t_prefill = time.time() - t0
+    toks_w, _, _ = m.generate_greedy([int(np.argmax(lg))], 0, warm_tokens)
+    n_timed = gen_len - warm_tokens
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    toks, _, gpu_ms = m.generate_greedy([int(toks_w[0, -1])], 0, n_timed)
+    t = torch.tensor([gpu_ms], dtype=torch.float64, device=dev)
+    ids = torch.from_numpy(np.concatenate([toks_w[0], toks[0]]).astype(np.int64)).to(dev)
+    gathered = [ids]
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        gathered = [torch.empty_like(ids) for _ in range(ws)]
+        torch.distributed.all_gather(gathered, ids)  # the final token-id gather of the sharded job
+    ms = float(t.item())
+    persist = m.persistent_decode()
+    m.close()
+    if ws > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        try:
+            os.remove(path)
+        except OSError:
+            pass
+    peaks, _ = measured_peaks()
+    avg_ctx = prompt_len + warm_tokens + n_timed / 2
+    kv_b = int(avg_ctx * cfg["num_hidden_layers"] * cfg["num_key_value_heads"] * cfg["head_dim"] * 2 * 2)
+    per_tok = wb + kv_b
+    ms_tok = ms / n_timed
+    return {
+        "metric": "LM decode tok/s (config 5 LM: Qwen3-4B shape, Q4_K_M, one sequence per GPU, greedy)",
+        "value": round(ws * n_timed / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": ws, "scaling": "weak",
+        "ms_per_token": round(ms_tok, 4),
+        "config": {"workload": "config5_lm4b_q4_k_m_decode", "prompt": prompt_len, "generated": gen_len,
+                   "timed_tokens_per_gpu": n_timed, "weights_MB": round(wb / 1e6, 1),
+                   "path": "persistent step" if persist else "per-op graph (Q4_K / Q6_K GEMVs)",
+                   "setup_s": {"gguf_write": round(t_gen, 1), "prefill": round(t_prefill, 2)}},
+        "hbm": {"bytes_per_token": per_tok, "bound_us_per_token": round(per_tok / (peaks["hbm_gbs"] * 1e3), 1),
+                "ratio_to_bound": round(ms_tok * 1e3 / (per_tok / (peaks["hbm_gbs"] * 1e3)), 3),
+                "achieved_GBs_per_gpu": round(per_tok / (ms_tok * 1e-3) / 1e9, 1)},
+        "tokens_gathered": int(sum(g.numel() for g in gathered)),
+        "tokens_head_rank0": toks_w[0, :4].tolist(),
+        "cpu_baseline": None,
+        "note": "no CPU sample for this sub-result (the 4B K-quant oracle needs minutes per token); "
+                "config 3's line carries the decode CPU baseline",
+    }
 
 
 ENC_S = 256
@@ -1190,10 +1285,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
-    ap.add_argument("--workloads", default="dit,ops,lm,enc",
+    ap.add_argument("--workloads", default="dit,ops,lm,enc,lm5",
                     help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
-                         "decode), enc (config 1 text encoder) -- the last three at N=1 as sub-results; without "
-                         "dit, ops is the headline; or one of gemv / gemm / enc / ditmodes alone")
+                         "decode), enc (config 1 text encoder) -- those three at N=1 as sub-results -- and lm5 "
+                         "(config 5's 4B Q4_K_M LM, one sequence per GPU, at every N); without dit, ops is the "
+                         "headline; or one of gemv / gemm / enc / ditmodes / lm5 alone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
