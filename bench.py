@@ -843,14 +843,10 @@ def run_lm5(dev, rank, ws, prompt_len=LM5_PROMPT, gen_len=LM5_GEN, warm_tokens=1
         torch.distributed.barrier()
     torch.cuda.synchronize()
     toks, _, gpu_ms = m.generate_greedy([int(toks_w[0, -1])], 0, n_timed)
-    t = torch.tensor([gpu_ms], dtype=torch.float64, device=dev)
+    import multi
     ids = torch.from_numpy(np.concatenate([toks_w[0], toks[0]]).astype(np.int64)).to(dev)
-    gathered = [ids]
-    if ws > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        gathered = [torch.empty_like(ids) for _ in range(ws)]
-        torch.distributed.all_gather(gathered, ids)  # the final token-id gather of the sharded job
-    ms = float(t.item())
+    gathered = multi.gather_rows(ids[None], ws)  # the final token-id gather of the sharded job
+    ms = multi.max_over_ranks(gpu_ms, ws, dev)
     persist = m.persistent_decode()
     m.close()
     if ws > 1:
@@ -876,7 +872,7 @@ def run_lm5(dev, rank, ws, prompt_len=LM5_PROMPT, gen_len=LM5_GEN, warm_tokens=1
         "hbm": {"bytes_per_token": per_tok, "bound_us_per_token": round(per_tok / (peaks["hbm_gbs"] * 1e3), 1),
                 "ratio_to_bound": round(ms_tok * 1e3 / (per_tok / (peaks["hbm_gbs"] * 1e3)), 3),
                 "achieved_GBs_per_gpu": round(per_tok / (ms_tok * 1e-3) / 1e9, 1)},
-        "tokens_gathered": int(sum(g.numel() for g in gathered)),
+        "tokens_gathered": int(gathered.numel()),
         "tokens_head_rank0": toks_w[0, :4].tolist(),
         "cpu_baseline": None,
         "note": "no CPU sample for this sub-result (the 4B K-quant oracle needs minutes per token); "
@@ -1089,13 +1085,17 @@ def run_dit_job(args, dev, rank, ws, local, stream):
     import acb
     import synthetic
 
+    import multi
+
     cfg = dict(synthetic.ACESTEP_DIT_2B)
     N, T, enc_S, Oc = DIT_TRACKS, DIT_T, DIT_ENC_S, cfg["out_channels"]
     Ng, S, ctx_ch = 2 * N, T // cfg["patch_size"], cfg["in_channels"] - Oc
-    if Ng % ws != 0:
-        raise SystemExit(f"the {Ng} sequences of config 4 do not shard over {ws} GPUs")
-    n_loc = Ng // ws
-    slots = list(range(rank * n_loc, (rank + 1) * n_loc))
+    try:
+        slots = multi.dit_slots(Ng, ws, rank)
+    except ValueError as e:
+        raise SystemExit(f"config 4: {e}")
+    n_loc = len(slots)
+    slot_track, slot_uncond = multi.slot_tracks(slots, N)
 
     def barrier():
         if ws > 1:
@@ -1119,15 +1119,14 @@ def run_dit_job(args, dev, rank, ws, local, stream):
     noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
     ctx = rng.standard_normal((N, T, ctx_ch)).astype(np.float32)
     enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
-    enc_loc = np.stack([enc[j] if j < N else np.broadcast_to(null, enc.shape[1:]) for j in slots])
+    enc_loc = np.stack([np.broadcast_to(null, enc.shape[1:]) if u else enc[tr] for tr, u in zip(slot_track, slot_uncond)])
     dit.set_condition(torch.from_numpy(np.ascontiguousarray(enc_loc)).to(dev), T)
-    tracks = torch.tensor([j % N for j in slots], device=dev)
+    tracks = torch.tensor(slot_track, device=dev)
     inp = torch.zeros((n_loc, T, cfg["in_channels"]), device=dev)
     inp[:, :, :ctx_ch] = torch.from_numpy(ctx).to(dev)[tracks]
     noise_d = torch.from_numpy(noise).to(dev)
     xt = noise_d.clone()
     vel_loc = torch.empty((n_loc, T, Oc), device=dev)
-    vel_all = torch.empty((Ng, T, Oc), device=dev) if ws > 1 else vel_loc
     vt = torch.empty((N, T, Oc), device=dev)
     x0 = torch.empty((N, T, Oc), device=dev)
     ra = torch.empty((N, T, Oc), dtype=torch.float64, device=dev)
@@ -1143,8 +1142,7 @@ def run_dit_job(args, dev, rank, ws, local, stream):
             tt.copy_(h_tt[0][i], non_blocking=True)
         inp[:, :, ctx_ch:] = xt[tracks]
         dit.eval(inp, tt, vel_loc)
-        if ws > 1:
-            torch.distributed.all_gather_into_tensor(vel_all, vel_loc)
+        vel_all = multi.gather_rows(vel_loc, ws)  # slot order: conditional tracks, then their twins
         acb.dit_apg(vel_all[:N], vel_all[N:], ra, i == 0, DIT_GUIDANCE, vt)
         last = i == DIT_STEPS - 1
         acb.dit_euler(xt, vt, tt, last, out=x0)
@@ -1163,12 +1161,7 @@ def run_dit_job(args, dev, rank, ws, local, stream):
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        ms = e0.elapsed_time(e1)
-        if ws > 1:
-            t = torch.tensor([ms], device=dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return multi.max_over_ranks(e0.elapsed_time(e1), ws, dev)
 
     peaks, kind = measured_peaks()
     fl = dit_step_flops(cfg, Ng, S, enc_S)
