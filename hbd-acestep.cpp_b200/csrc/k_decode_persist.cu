@@ -66,10 +66,10 @@ constexpr int kSmFull   = 0;     // uint64 full[16]
 constexpr int kSmEmpty  = 128;   // uint64 empty[16]
 constexpr int kSmRed    = 256;   // double [16][4]
 constexpr int kSmMisc   = 768;   // float inv[4], int flags
-constexpr int kSmTred   = 1024;  // float [2][8 warps][16 rows]
 constexpr int kSmGate   = 2048;  // float [256] gate rows of this CTA's SwiGLU tiles; residual rows
 constexpr int kSmAct    = 3072;  // int8 xq[kPdMaxK] + float xd[kPdMaxK/32]; attention scratch
-constexpr int kSmRing   = (kSmAct + kPdMaxK + kPdMaxK / 32 * 4 + 127) / 128 * 128;
+constexpr int kSmTredG  = kSmAct + kPdMaxK + kPdMaxK / 32 * 4;  // float [8 tiles][8 warps][16 rows]
+constexpr int kSmRing   = (kSmTredG + kPdWarps * kPdWarps * 16 * 4 + 127) / 128 * 128;
 // attention scratch inside the activation region
 constexpr int kAtQ      = 0;      // float [G][128] f16-rounded q
 constexpr int kAtKp     = 2048;   // float [128] the new k (f16-rounded)
@@ -85,7 +85,7 @@ __device__ __forceinline__ double * sm_red() { return reinterpret_cast<double *>
 __device__ __forceinline__ float * sm_misc() { return reinterpret_cast<float *>(pd_smem + kSmMisc); }
 __device__ __forceinline__ volatile int * sm_abort() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 32); }
 __device__ __forceinline__ volatile int * sm_last() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 36); }
-__device__ __forceinline__ float * sm_tred() { return reinterpret_cast<float *>(pd_smem + kSmTred); }
+__device__ __forceinline__ float * sm_tredg() { return reinterpret_cast<float *>(pd_smem + kSmTredG); }
 __device__ __forceinline__ uint8_t * sm_act() { return pd_smem + kSmAct; }
 __device__ __forceinline__ float * sm_gate() { return reinterpret_cast<float *>(pd_smem + kSmGate); }
 __device__ __forceinline__ int8_t * sm_xq() { return reinterpret_cast<int8_t *>(pd_smem + kSmAct); }
@@ -305,7 +305,6 @@ __device__ void pd_producer(const PdParams & P) {
 // ---- consumer pieces --------------------------------------------------------------------------
 struct PdCtx {
     uint32_t it;     // ring stage counter (the producer's issue order)
-    int      tbuf;   // tile-reduction buffer parity
     unsigned epoch;  // grid barriers passed
 };
 
@@ -524,7 +523,14 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
     pd_range(n_rows / 16, gi, blockIdx.x, P.n_ctas, t0, t1);
     const int        nb  = K / 32;
     const uint32_t * xq4 = reinterpret_cast<const uint32_t *>(sm_xq());
-    for (int64_t t = t0; t < t1; t++) {
+    if (EPI == EPI_UP) {
+        cons_sync();  // the gate GEMV's reducers are done with the partials buffer
+    }
+    // tiles in groups of (up to) 8: every warp leaves its partials of each tile of the group in
+    // shared memory, one named barrier, then warp j adds tile j's partials in warp order
+    for (int64_t tg = t0; tg < t1; tg += kPdWarps) {
+        const int nt = (int) min((int64_t) kPdWarps, t1 - tg);
+        for (int j = 0; j < nt; j++) {
         float acc0 = 0.0f, acc2 = 0.0f;  // rows g and g + 8, this lane's 8 of every 32 columns
         for (int b0 = 0; b0 < nb; b0 += bs) {
             const int       s    = (int) (x.it % (uint32_t) P.slots);
@@ -591,14 +597,17 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
         acc2 = __fadd_rn(acc2, __shfl_xor_sync(0xffffffffu, acc2, 1));
         acc0 = __fadd_rn(acc0, __shfl_xor_sync(0xffffffffu, acc0, 2));
         acc2 = __fadd_rn(acc2, __shfl_xor_sync(0xffffffffu, acc2, 2));
-        float * tr = sm_tred() + x.tbuf * (kPdWarps * 16);
         if (q == 0) {
-            tr[warp * 16 + g]     = acc0;
-            tr[warp * 16 + g + 8] = acc2;
+            float * tr = sm_tredg() + (j * kPdWarps + warp) * 16;
+            tr[g]      = acc0;
+            tr[g + 8]  = acc2;
+        }
         }
         cons_sync();
-        if (warp == (int) ((t - t0) & (kPdWarps - 1)) && lane < 16) {
-            float v = 0.0f;
+        if (warp < nt && lane < 16) {
+            const int64_t t  = tg + warp;
+            const float * tr = sm_tredg() + warp * kPdWarps * 16;
+            float         v  = 0.0f;
 #pragma unroll
             for (int w = 0; w < kPdWarps; w++) {
                 v = __fadd_rn(v, tr[w * 16 + lane]);
@@ -617,7 +626,9 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
                 best_push(best, v, (int) row);
             }
         }
-        x.tbuf ^= 1;
+        if (tg + kPdWarps < t1) {
+            cons_sync();  // the next group reuses the partials buffer
+        }
     }
     return *sm_abort() == 0;
 }
@@ -1030,7 +1041,6 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
     const int               tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     PdCtx                   x;
     x.it      = 0;
-    x.tbuf    = 0;
     x.epoch   = 0;
 
     // step inputs: every CTA reads the same values and takes the same exit
