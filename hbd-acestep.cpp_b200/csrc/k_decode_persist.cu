@@ -30,10 +30,10 @@
 // copies in flight before its CTA exits.
 //
 // Arithmetic per op is that of the per-op kernels: activation quantisation of quantize_q8_0,
-// the per-block scaled int8 MMA of gemv_tiles_kernel, q/k-norm + RoPE of qkv_post_kernel, the
-// two-pass f16-cache softmax of attn_scores_kernel / attn_pv_kernel, the argmax of
-// argmax_kernel. Only the partition (16 warps, split count, tile ranges) decides summation
-// orders, as it does there.
+// exact integer dot products per Q8_0 block scaled by d_w * d_x (dp4a here, the int8 MMA of
+// gemv_tiles_kernel there), q/k-norm + RoPE of qkv_post_kernel, the two-pass f16-cache softmax
+// of attn_scores_kernel / attn_pv_kernel, the argmax of argmax_kernel. Only the partition (8
+// consumer warps, 4 lanes per row, split count, tile ranges) decides the order of the float sums.
 #include <cstdlib>
 #include <string>
 
@@ -73,7 +73,7 @@ constexpr int kSmRing   = (kSmTredG + kPdWarps * kPdWarps * 16 * 4 + 127) / 128 
 // attention scratch inside the activation region
 constexpr int kAtQ      = 0;      // float [G][128] f16-rounded q
 constexpr int kAtKp     = 2048;   // float [128] the new k (f16-rounded)
-constexpr int kAtAcc    = 2560;   // float4 [16 warps][32]
+constexpr int kAtAcc    = 2560;   // float4 [8 warps][32] (P.V partials; the combine uses 256)
 constexpr int kAtMax    = 10752;  // float [16][G]
 
 extern __shared__ __align__(128) uint8_t pd_smem[];
@@ -501,9 +501,9 @@ __device__ __forceinline__ void pd_block(const uint4 & a, uint32_t dw, uint2 xw,
     acc2           = __fmaf_rn((float) s1, __fmul_rn(dh, dx), acc2);
 }
 
-// Tensor-core Q8_0 tile GEMV over this CTA's tile range (gemv_tiles_kernel arithmetic for one
-// activation column): warp w takes blocks w, w + 16, ... of every stage; at the end of a tile
-// the 16 warps' partials are added in warp order by one warp (rotating) and stored.
+// Q8_0 tile GEMV over this CTA's tile range for one activation column: warp w takes 8
+// consecutive K-blocks of every stage (pd_block), its lanes' partials are added over the 4
+// lanes of a row, and the 8 warps' partials of a tile are added in warp order by one warp.
 // Residual row of the reducer lane (lane < 16) of warp w for EPI_ADD GEMV gi: y[(t0 + w) * 16 +
 // lane]. Requested a whole stage ahead of the GEMV (the rows last changed two barriers earlier),
 // so the epilogue finds it in a register.
