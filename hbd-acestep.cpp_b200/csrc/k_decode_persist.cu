@@ -237,25 +237,26 @@ __device__ void pd_producer(const PdParams & P) {
     volatile int * s_abort = sm_abort();
     const acb_decode_step & S     = P.s;
     const uint64_t          pol   = ptx::policy_evict_first();
-    const int               nseg  = 5 * S.n_layers + 1;
+    const int               nseg  = (5 * S.n_layers + 1) * max(1, S.n_steps);  // every step streams all weights
     uint32_t                it    = 0;
     bool                    ok    = true;
     // prefetch cursor
     int             pk = 0, pK, pbs;
     int64_t         po = 0, pb, pref = 0, loaded = 0;
     const uint8_t * pp;
+    const int       per = 5 * S.n_layers + 1;
     pd_segment(P, 0, pp, pb, pK, pbs);
     for (int k = 0; k < nseg && ok; k++) {
         const uint8_t * W;
         int64_t         seg_bytes;
         int             K, bs;
-        pd_segment(P, k, W, seg_bytes, K, bs);
+        pd_segment(P, k % per, W, seg_bytes, K, bs);
         const uint32_t bytes = (uint32_t) bs * kPdTileBlk;
         for (int64_t off = 0; off < seg_bytes && ok; off += bytes) {
             while (pref < loaded + P.prefetch && pk < nseg) {
                 if (po >= pb) {
                     if (++pk < nseg) {
-                        pd_segment(P, pk, pp, pb, pK, pbs);
+                        pd_segment(P, pk % per, pp, pb, pK, pbs);
                         po = 0;
                     }
                     continue;
@@ -1044,10 +1045,12 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
     x.epoch   = 0;
 
     // step inputs: every CTA reads the same values and takes the same exit
-    const int id = __ldcg(S.ids), p = __ldcg(S.pos);
-    if (id < 0 || id >= S.embed_rows || p < 0 || p >= S.max_seq || p >= S.max_pos) {
+    const int n_steps = max(1, S.n_steps);
+    const int id0 = __ldcg(S.ids), p0 = __ldcg(S.pos);
+    const int p_last  = p0 + n_steps - 1;
+    if (id0 < 0 || id0 >= S.embed_rows || p0 < 0 || p_last >= S.max_seq || p_last >= S.max_pos) {
         if (blockIdx.x == 0 && tid == 0 && S.err) {
-            atomicOr(S.err, (id < 0 || id >= S.embed_rows) ? ACB_DEVERR_ID_RANGE : ACB_DEVERR_POS_RANGE);
+            atomicOr(S.err, (id0 < 0 || id0 >= S.embed_rows) ? ACB_DEVERR_ID_RANGE : ACB_DEVERR_POS_RANGE);
         }
         return;
     }
@@ -1069,8 +1072,11 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
     }
 
     const int qd = S.n_heads * S.head_dim, qkvd = qd + 2 * S.n_kv_heads * S.head_dim;
+    bool      ok = true;
+    int       id = id0;
+    for (int tok = 0; tok < n_steps; tok++) {
+    const int p    = p0 + tok;
     Best      best = { -INFINITY, -INFINITY, 0x7fffffff };
-    bool      ok   = true;
     for (int l = 0; l < S.n_layers && ok; l++) {
         const acb_decode_layer & L = S.layers[l];
         if (l == 0) {
@@ -1115,7 +1121,7 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
     if (!pd_gemv<EPI_HEAD>(P, x, S.vocab, S.hidden, P.bs_h, 4 * S.n_layers, S.logits, best)) {
         return;
     }
-    // CTA best -> partial; the last CTA merges in CTA order and finishes the step
+    // CTA best -> partial
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         best_merge(best, __shfl_xor_sync(0xffffffffu, best.b1, o), __shfl_xor_sync(0xffffffffu, best.b2, o),
@@ -1126,6 +1132,7 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
         wb[warp] = make_float4(best.b1, best.b2, __int_as_float(best.i1), 0.0f);
     }
     cons_sync();
+    const bool last_step = tok + 1 == n_steps;
     if (tid == 0) {
         Best r = { -INFINITY, -INFINITY, 0x7fffffff };
         for (int w = 0; w < kPdWarps; w++) {
@@ -1133,9 +1140,44 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
             best_merge(r, v.x, v.y, __float_as_int(v.z));
         }
         __stcg(P.bpart + blockIdx.x, make_float4(r.b1, r.b2, __int_as_float(r.i1), 0.0f));
-        __threadfence();
-        const int tk = atomicAdd(P.done, 1);
-        *sm_last()    = (tk == P.n_ctas - 1);
+        if (last_step) {
+            __threadfence();
+            const int tk = atomicAdd(P.done, 1);
+            *sm_last()    = (tk == P.n_ctas - 1);
+        }
+    }
+    if (!last_step) {
+        // a following step of the same launch: after a grid barrier every CTA merges the CTA
+        // partials in CTA order (the same triple everywhere), CTA 0 records the token
+        if (!pd_grid_sync(P, x)) {
+            return;
+        }
+        if (warp == 0) {
+            Best r = { -INFINITY, -INFINITY, 0x7fffffff };
+            for (int k = lane; k < P.n_ctas; k += 32) {
+                const float4 v = __ldcg(P.bpart + k);
+                best_merge(r, v.x, v.y, __float_as_int(v.z));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                best_merge(r, __shfl_xor_sync(0xffffffffu, r.b1, o), __shfl_xor_sync(0xffffffffu, r.b2, o),
+                           __shfl_xor_sync(0xffffffffu, r.i1, o));
+            }
+            if (lane == 0) {
+                *sm_last() = r.i1;  // the next token, for the whole CTA
+                if (blockIdx.x == 0 && S.hist && S.hist_base) {
+                    const int step = p - S.hist_base[0];
+                    S.hist[step]   = r.i1;
+                    if (S.mhist) {
+                        S.mhist[step] = r.b1 - r.b2;
+                    }
+                }
+            }
+        }
+        cons_sync();
+        id = *sm_last();
+        cons_sync();  // every thread has the token before sm_last is written again
+        continue;
     }
     cons_sync();
     if (!*sm_last() || warp != 0) {
@@ -1170,6 +1212,7 @@ __global__ void __launch_bounds__(kPdThreads, 1) lm_decode_kernel(const PdParams
         // every CTA has passed its last barrier: the counters return to zero for the next step
         *P.done = 0;
         *P.bar  = 0;
+    }
     }
 }
 

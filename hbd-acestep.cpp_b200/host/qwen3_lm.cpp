@@ -258,11 +258,13 @@ void setup_persistent(acb_qw3lm * m) {
     m->persist = true;
 }
 
-// One persistent step for kv set `set` (ids/pos already on the device).
-acb_status persistent_step(acb_qw3lm * m, int set, bool greedy) {
+// One persistent launch for kv set `set` (ids/pos already on the device): one step, or n_steps
+// greedy steps that feed each argmax to the next.
+acb_status persistent_step(acb_qw3lm * m, int set, bool greedy, int n_steps = 1) {
     acb_decode_step p = m->pd;
     p.kv_set          = set;
     p.greedy          = greedy ? 1 : 0;
+    p.n_steps         = greedy ? n_steps : 1;
     if (greedy) {
         p.hist      = m->hist.as<int32_t>();
         p.mhist     = m->mhist.as<float>();
@@ -705,8 +707,15 @@ extern "C" acb_status acb_qw3lm_generate_greedy(acb_qw3lm * m, const int32_t * l
     int               hv    = 0;
     const DevTensor * ghead = head_for(m, 0, 0, &hv);
     const bool        pers  = N == 1 && m->persist;
-    for (int k = 0; k < n_steps && s == ACB_OK; k++) {
-        s = pers ? persistent_step(m, set0, true) : run_graph(m, key, N, set0, ghead, hv, true, false);
+    if (pers) {
+        // up to 64 tokens per launch (each launch ends with the counters back at zero)
+        for (int k = 0; k < n_steps && s == ACB_OK; k += 64) {
+            s = persistent_step(m, set0, true, std::min(64, n_steps - k));
+        }
+    } else {
+        for (int k = 0; k < n_steps && s == ACB_OK; k++) {
+            s = run_graph(m, key, N, set0, ghead, hv, true, false);
+        }
     }
     cudaEventRecord(e1, m->st);
     if (s == ACB_OK) {

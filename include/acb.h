@@ -493,6 +493,8 @@ typedef struct acb_decode_step {
     int32_t *     pos;        /* [1] kv position of this step; += 1 when greedy */
     float *       logits;     /* [vocab] */
     int           greedy;     /* 1: argmax -> ids[0], margin, history, pos[0] += 1 */
+    int           n_steps;    /* greedy tokens decoded by this launch (each step feeds the last argmax;
+                                 <= 1: one step); history holds every step, ids / pos / margin the last */
     float *       margin;     /* [1] top1 - top2, or NULL */
     int32_t *     hist;       /* token history [max_seq] at pos - hist_base[0], or NULL */
     float *       mhist;      /* margin history, or NULL */

@@ -63,7 +63,7 @@ class _DecodeStep(C.Structure):
                 ("attn_scale", C.c_float), ("max_seq", C.c_int), ("max_pos", C.c_int), ("kv_set", C.c_int),
                 ("embed", C.c_void_p), ("embed_rows", C.c_int64), ("head", C.c_void_p), ("vocab", C.c_int64),
                 ("final_norm", C.c_void_p), ("rope", C.c_void_p), ("ids", C.c_void_p), ("pos", C.c_void_p),
-                ("logits", C.c_void_p), ("greedy", C.c_int), ("margin", C.c_void_p), ("hist", C.c_void_p),
+                ("logits", C.c_void_p), ("greedy", C.c_int), ("n_steps", C.c_int), ("margin", C.c_void_p), ("hist", C.c_void_p),
                 ("mhist", C.c_void_p), ("hist_base", C.c_void_p), ("scratch", C.c_void_p), ("err", C.c_void_p)]
 
 
