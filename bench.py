@@ -786,7 +786,7 @@ def run_lm(dev, rank, warm_tokens=16, want_cpu=True, gguf_dir=None, prompt_len=L
                 "frac_of_measured": round(per_tok_bytes * tok_s / 1e9 / peaks["hbm_gbs"], 4),
                 "bound_us_per_token": round(per_tok_bytes / (peaks["hbm_gbs"] * 1e3), 1),
                 "ratio_to_bound": round((gpu_ms / n_timed * 1e3) / (per_tok_bytes / (peaks["hbm_gbs"] * 1e3)), 3)},
-        "path": "persistent (acb_lm_decode_step, one launch per token)" if persist else "per-op graph",
+        "path": "persistent (acb_lm_decode_step, up to 64 greedy tokens per launch)" if persist else "per-op graph",
         "roofline": ({"kernel": "lm_decode_kernel (whole step: weights + KV cache bytes per token)", "bound": "hbm",
                       "achieved": round(step_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": round(step_gbs / peaks["hbm_gbs"], 4), "traffic": None} if persist else

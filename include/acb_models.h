@@ -199,10 +199,11 @@ ACB_API void       acb_qw3lm_reset_kv(acb_qw3lm * m, int kv_set);            /* 
 ACB_API acb_status acb_qw3lm_copy_kv(acb_qw3lm * m, int src, int dst);       /* qw3lm_copy_kv :233 */
 ACB_API acb_status acb_qw3lm_build_partial_head(acb_qw3lm * m, int lm_offset); /* :290 */
 ACB_API int        acb_qw3lm_kv_pos(const acb_qw3lm * m, int kv_set);
-/* 1 when single-sequence decode (acb_qw3lm_forward_batch with N = 1 and the full head, and
- * acb_qw3lm_generate_greedy with N = 1) runs as one persistent launch per token
- * (acb_lm_decode_step); 0 when it runs the per-op graph (shape outside the persistent kernel,
- * or ACB_LM_PERSIST=0 in the environment at load). No counterpart in the reference. */
+/* 1 when single-sequence decode runs as the persistent step (acb_lm_decode_step):
+ * acb_qw3lm_forward_batch with N = 1 and the full head (one launch per call), and
+ * acb_qw3lm_generate_greedy with N = 1 (up to 64 tokens per launch); 0 when it runs the per-op
+ * graph (shape outside the persistent kernel, e.g. K-quant weights, or ACB_LM_PERSIST=0 in the
+ * environment at load). No counterpart in the reference. */
 ACB_API int        acb_qw3lm_persistent_decode(const acb_qw3lm * m);
 ACB_API void       acb_qw3lm_free(acb_qw3lm * m);                             /* qw3lm_free :826 */
 
