@@ -91,7 +91,7 @@ def test_gemm_split_k(cuda, M, N, K):
     import torch
     ws_bytes = acb.gemm_workspace_bytes(M, N, K)
     assert ws_bytes > 0, "these shapes are meant to split"
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=cuda)
     g = torch.Generator(device=cuda).manual_seed(M + N * 3 + K)
     A = torch.randn(M, K, device=cuda, generator=g).half()
     B = (torch.randn(N, K, device=cuda, generator=g) * 0.05).half()
@@ -116,6 +116,31 @@ def test_gemm_split_k(cuda, M, N, K):
     assert (d <= base.abs() * 2.0 ** -10 + 2e-5 * base.abs().max()).all()
 
 
+def test_gemm_split_k_shared_workspace(cuda):
+    """Split GEMMs of different shapes take turns on one workspace (as a model's linears do): the
+    tile counters keep their place whatever the partials of the other shapes cover, so every call
+    still matches its own result on a fresh workspace, bit for bit."""
+    import torch
+    shapes = [(77, 1024, 2048), (256, 6144, 1024), (1, 2048, 6144), (256, 1024, 3072)]
+    need = max(acb.gemm_workspace_bytes(*s) for s in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(7)
+    ops = [(torch.randn(M, K, device=cuda, generator=g).half(),
+            (torch.randn(N, K, device=cuda, generator=g) * 0.05).half()) for M, N, K in shapes]
+    want = []
+    for (A, B), s in zip(ops, shapes):
+        own = torch.zeros(acb.gemm_workspace_bytes(*s), dtype=torch.uint8, device=cuda)
+        want.append(acb.gemm_bf16(A, B, workspace=own))
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for rep in range(3):
+        for i in (list(range(len(shapes))) if rep % 2 == 0 else reversed(range(len(shapes)))):
+            A, B = ops[i]
+            got = acb.gemm_bf16(A, B, workspace=ws, err=err)
+            assert torch.equal(got, want[i]), (rep, shapes[i])
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(256, 1024, 3072), (300, 512, 1024)])
 def test_gemm_exact_split_products(cuda, M, N, K):
     """GEMM over K' = 3K with A' = [hi|hi|lo] and B' = [hi|lo|hi] (acb_act_quant_ex layouts): the
@@ -129,7 +154,7 @@ def test_gemm_exact_split_products(cuda, M, N, K):
     xd = O.dequantize(O.quantize(x, O.Q8_0), O.Q8_0, K)
     A = acb.act_quant_ex(torch.from_numpy(x).to(cuda), K, O.Q8_0, acb.LAYOUT_GEMM_A)
     B = acb.act_quant_ex(torch.from_numpy(wd).to(cuda), K, O.F16, acb.LAYOUT_GEMM_B)
-    ws = torch.empty(max(1, acb.gemm_workspace_bytes(M, N, 3 * K)), dtype=torch.uint8, device=cuda)
+    ws = torch.zeros(max(1, acb.gemm_workspace_bytes(M, N, 3 * K)), dtype=torch.uint8, device=cuda)
     C = acb.gemm_bf16(A, B, workspace=ws).double().cpu().numpy()
     ref = xd.astype(np.float64) @ wd.astype(np.float64).T
     assert max_rel(C, ref) <= 2e-6, max_rel(C, ref)
