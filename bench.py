@@ -432,6 +432,10 @@ def run_ops_line(args, dev, rank, ws, local, stream):
     torch.cuda.synchronize()
     clk.start()
     time.sleep(0.3)
+    # a ~2 ms spin on the stream first, so that the host's launches (ctypes calls from Python,
+    # slower than these 20-90 us kernels are short) queue up ahead of the GPU and the events
+    # time the kernels back to back rather than the host's launch gaps
+    torch.cuda._sleep(4_000_000)
     t_start.record(stream)
     for k in range(args.steps):
         for (ea, eb), (_io, _n, f, _b) in zip(evs[k], ops):

@@ -1,8 +1,9 @@
 // k_rowops.cu -- row-wise ops of the op-chain: RMSNorm (+weight), adaLN modulate (with the
 // fused RMSNorm), per-head q/k RMSNorm + NeoX RoPE with strided / KV-cache destinations.
 //
-// All three are HBM-bound: one warp owns one row (or one head), the row is loaded once with
-// 16-byte vector loads into registers, reduced with warp shuffles, and written once. The
+// All three are HBM-bound: one CTA owns one row (a warp for very wide rows; a warp takes a few
+// heads), the row is loaded once with 16-byte vector loads into registers, reduced with
+// shuffles, and written once. The
 // sum of squares is accumulated in double (the ggml-CPU rule), which makes the normalisation
 // scale identical to the CPU's; products and sums that ggml performs as separate graph nodes
 // are kept separately rounded (__fmul_rn / __fadd_rn) so no multiply-add is contracted.
@@ -45,91 +46,126 @@ template <int N> __device__ __forceinline__ void load_w(const float * w, float *
     }
 }
 
-// ---- RMSNorm / adaLN: one warp per row, row cached in registers ---------------------------
+// ---- RMSNorm / adaLN: a CTA per row at a time, grid-stride with one row of lookahead -------
 // MODE 0: y = rms_norm(x)*w (w may be null)
 // MODE 1: y = (w ? rms_norm(x)*w : x) * (1 + scale) + shift
-template <int TI, int TO, int MAXV, int MODE>
-__global__ void __launch_bounds__(256) row_norm_kernel(const void * __restrict__ x, int64_t xs,
-                                                       const float * __restrict__ w, void * __restrict__ y,
-                                                       int64_t ys, int64_t rows, int cols, float eps,
-                                                       const float * __restrict__ scale,
-                                                       const float * __restrict__ shift, int64_t vec_stride,
-                                                       int64_t rows_per_sample) {
-    using VI              = vec16<TI>;
-    constexpr int N       = VI::N;
-    using ei              = typename io<TI>::t;
-    using eo              = typename io<TO>::t;
-    const int     lane    = threadIdx.x & 31;
-    const int64_t row     = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+// A row is spread over the CTA (V 16-byte vectors per thread, vector i*blockDim + tid). The grid
+// is as many CTAs as fit on the SMs at once; each walks rows r, r + grid, ... and loads the next
+// row while it reduces, scales and stores the current one, so HBM reads never stop for the
+// reduction or for launching a new CTA. The double sum of squares is reduced with warp shuffles,
+// then over the warps' sums in warp order.
+template <int TI, int TO, int V, int MODE>
+__global__ void __launch_bounds__(512) row_norm_cta_kernel(const void * __restrict__ x, int64_t xs,
+                                                            const float * __restrict__ w, void * __restrict__ y,
+                                                            int64_t ys, int64_t rows, int cols, float eps,
+                                                            const float * __restrict__ scale,
+                                                            const float * __restrict__ shift, int64_t vec_stride,
+                                                            int64_t rows_per_sample) {
+    using VI          = vec16<TI>;
+    constexpr int N   = VI::N;
+    using ei          = typename io<TI>::t;
+    using eo          = typename io<TO>::t;
+    __shared__ double red[2][32];  // two slots: a fast warp may start the next row's sum early
+    const int     tid     = threadIdx.x;
+    const int     nt      = blockDim.x;
+    const int     nvec    = cols / N;
+    const bool    do_norm = (MODE == 0) || (w != nullptr);
+    const int64_t stride  = gridDim.x;
+
+    VI cur[V], nxt[V];
+    int64_t row = blockIdx.x;
     if (row >= rows) {
         return;
     }
-    const char * xr   = reinterpret_cast<const char *>(x) + row * xs * (int64_t) sizeof(ei);
-    char *       yr   = reinterpret_cast<char *>(y) + row * ys * (int64_t) sizeof(eo);
-    const int    nvec = cols / N;
-
-    VI     v[MAXV];
-    double ss = 0.0;
+    {
+        const char * xr = reinterpret_cast<const char *>(x) + row * xs * (int64_t) sizeof(ei);
 #pragma unroll
-    for (int i = 0; i < MAXV; i++) {
-        const int vi = lane + i * 32;
-        if (vi < nvec) {
-            v[i].load_stream(xr + (int64_t) vi * 16);
+        for (int i = 0; i < V; i++) {
+            const int vi = tid + i * nt;
+            if (vi < nvec) {
+                cur[i].load_stream(xr + (int64_t) vi * 16);
+            }
         }
     }
-    const bool do_norm = (MODE == 0) || (w != nullptr);
-    if (do_norm) {
+    for (int it = 0; row < rows; row += stride, it ^= 1) {
+        const int64_t nrow = row + stride;
+        if (nrow < rows) {
+            const char * xr = reinterpret_cast<const char *>(x) + nrow * xs * (int64_t) sizeof(ei);
 #pragma unroll
-        for (int i = 0; i < MAXV; i++) {
-            const int vi = lane + i * 32;
-            if (vi < nvec) {
-#pragma unroll
-                for (int j = 0; j < N; j++) {
-                    float f = v[i].get(j);
-                    ss += (double) __fmul_rn(f, f);
+            for (int i = 0; i < V; i++) {
+                const int vi = tid + i * nt;
+                if (vi < nvec) {
+                    nxt[i].load_stream(xr + (int64_t) vi * 16);
                 }
             }
         }
-        ss = warp_sum(ss);
-    }
-    const float sc = do_norm ? rms_scale(ss, cols, eps) : 1.0f;
-    const float * scl = nullptr;
-    const float * shf = nullptr;
-    if (MODE == 1) {
-        const int64_t s = row / rows_per_sample;
-        scl             = scale + s * vec_stride;
-        shf             = shift + s * vec_stride;
-    }
+        float sc = 1.0f;
+        if (do_norm) {
+            double ss = 0.0;
 #pragma unroll
-    for (int i = 0; i < MAXV; i++) {
-        const int vi = lane + i * 32;
-        if (vi < nvec) {
-            float o[N];
-            float wv[N];
-            if (w) {
-                load_w<N>(w + (int64_t) vi * N, wv);
-            }
+            for (int i = 0; i < V; i++) {
+                if (tid + i * nt < nvec) {
 #pragma unroll
-            for (int j = 0; j < N; j++) {
-                float f = v[i].get(j);
-                if (do_norm) {
-                    f = __fmul_rn(f, sc);
-                    if (w) {
-                        f = __fmul_rn(f, wv[j]);
+                    for (int j = 0; j < N; j++) {
+                        const float f = cur[i].get(j);
+                        ss += (double) __fmul_rn(f, f);
                     }
                 }
-                o[j] = f;
             }
-            if (MODE == 1) {
-                float a[N], b[N];
-                load_w<N>(scl + (int64_t) vi * N, a);
-                load_w<N>(shf + (int64_t) vi * N, b);
+            ss = warp_sum(ss);
+            if ((tid & 31) == 0) {
+                red[it][tid >> 5] = ss;
+            }
+            __syncthreads();
+            double t = 0.0;
+            for (int k = 0; k < (nt >> 5); k++) {  // every thread sums the warps' sums in warp order
+                t += red[it][k];
+            }
+            sc = rms_scale(t, cols, eps);
+        }
+        const float * scl = nullptr;
+        const float * shf = nullptr;
+        if (MODE == 1) {
+            const int64_t smp = row / rows_per_sample;
+            scl               = scale + smp * vec_stride;
+            shf               = shift + smp * vec_stride;
+        }
+        char * yr = reinterpret_cast<char *>(y) + row * ys * (int64_t) sizeof(eo);
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            const int vi = tid + i * nt;
+            if (vi < nvec) {
+                float o[N];
+                float wv[N];
+                if (w) {
+                    load_w<N>(w + (int64_t) vi * N, wv);
+                }
 #pragma unroll
                 for (int j = 0; j < N; j++) {
-                    o[j] = __fadd_rn(__fmul_rn(o[j], __fadd_rn(a[j], 1.0f)), b[j]);
+                    float f = cur[i].get(j);
+                    if (do_norm) {
+                        f = __fmul_rn(f, sc);
+                        if (w) {
+                            f = __fmul_rn(f, wv[j]);
+                        }
+                    }
+                    o[j] = f;
                 }
+                if (MODE == 1) {
+                    float a[N], b[N];
+                    load_w<N>(scl + (int64_t) vi * N, a);
+                    load_w<N>(shf + (int64_t) vi * N, b);
+#pragma unroll
+                    for (int j = 0; j < N; j++) {
+                        o[j] = __fadd_rn(__fmul_rn(o[j], __fadd_rn(a[j], 1.0f)), b[j]);
+                    }
+                }
+                store_n<TO, N>(yr + (int64_t) vi * N * (int64_t) sizeof(eo), o);
             }
-            store_n<TO, N>(yr + (int64_t) vi * N * (int64_t) sizeof(eo), o);
+        }
+#pragma unroll
+        for (int i = 0; i < V; i++) {
+            cur[i] = nxt[i];
         }
     }
 }
@@ -192,20 +228,24 @@ static acb_status launch_row_norm(const void * x, int64_t xs, const float * w, v
                                         (reinterpret_cast<uintptr_t>(shift) % 16) == 0 && vs % 4 == 0)) &&
                          (NI * so) >= 8;
     const int nvec = cols / NI;
-    if (aligned && nvec <= 32 * 24) {
-        if (nvec <= 32 * 4) {
-            row_norm_kernel<TI, TO, 4, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
-                                                                         shift, vs, rps);
-        } else if (nvec <= 32 * 8) {
-            row_norm_kernel<TI, TO, 8, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
-                                                                         shift, vs, rps);
-        } else if (nvec <= 32 * 16) {
-            row_norm_kernel<TI, TO, 16, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
-                                                                          shift, vs, rps);
-        } else {
-            row_norm_kernel<TI, TO, 24, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
-                                                                          shift, vs, rps);
+    if (aligned && nvec <= 4 * 512) {
+        // a row per CTA at a time, 4 vectors per thread: 32..512 threads; as many CTAs as are
+        // resident at once (per block size, cached)
+        const int threads = ((nvec + 4 * 32 - 1) / (4 * 32)) * 32;
+        static int resident[17];
+        int &      res = resident[threads / 32];
+        if (res == 0) {
+            int per_sm = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_norm_cta_kernel<TI, TO, 4, MODE>, threads,
+                                                              0) != cudaSuccess ||
+                per_sm < 1) {
+                per_sm = 1;
+            }
+            res = per_sm * num_sms();
         }
+        const int64_t nb = rows < res ? rows : res;
+        row_norm_cta_kernel<TI, TO, 4, MODE><<<dim3((unsigned) nb), threads, 0, st>>>(x, xs, w, y, ys, rows, cols,
+                                                                                   eps, scale, shift, vs, rps);
     } else {
         row_norm_scalar_kernel<TI, TO, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
                                                                           shift, vs, rps);
@@ -233,10 +273,11 @@ static acb_status dispatch_row_norm(int ti, int to, const void * x, int64_t xs, 
 }
 
 // ---- per-head q/k RMSNorm + NeoX RoPE ------------------------------------------------------
-// One warp per (token, head). Lane l owns E = D/64 consecutive elements of the first half
-// starting at l*E and the matching elements of the second half, so each NeoX pair (i, i+D/2)
-// lives in one lane.
-template <int TI, int TO, int E>
+// One warp per HPW consecutive (token, head) items. Lane l owns E = D/64 consecutive elements of
+// the first half starting at l*E and the matching elements of the second half, so each NeoX pair
+// (i, i+D/2) lives in one lane. The warp issues the loads of all its heads before any reduction,
+// so a head of 256-512 bytes does not leave the warp waiting on one round trip per head.
+template <int TI, int TO, int E, int HPW>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const void * __restrict__ src, int64_t sts, void * __restrict__ dst, int64_t dts, int64_t dhs, int64_t dps,
     int64_t n_tok, int n_heads, const float * __restrict__ w, float eps, const int32_t * __restrict__ pos,
@@ -246,62 +287,110 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     constexpr int D       = 64 * E;
     constexpr int HALF    = D / 2;
     const int     lane    = threadIdx.x & 31;
-    const int64_t item    = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (item >= n_tok * n_heads) {
+    const int64_t items   = n_tok * n_heads;
+    const int64_t item0   = ((int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW;
+    if (item0 >= items) {
         return;
     }
-    const int64_t t = item / n_heads;
-    const int     h = (int) (item - t * n_heads);
-    int           p = 0;
-    if (pos) {
-        p = __ldg(pos + t);
-        if (p < 0 || p >= max_pos) {
+    // every load of the warp's heads is issued before the first use: positions, the head
+    // vectors, the norm weights, then the rope rows (which wait only on the positions)
+    // (token, head) of each item: one division per warp, then steps of one head (items past the
+    // end are clamped to the last item so that their loads stay in bounds)
+    int64_t tk[HPW];
+    int     hd[HPW];
+    {
+        int64_t t = item0 / n_heads;
+        int     h = (int) (item0 - t * n_heads);
+#pragma unroll
+        for (int k = 0; k < HPW; k++) {
+            const bool in = item0 + k < items;
+            tk[k]         = in ? t : (items - 1) / n_heads;
+            hd[k]         = in ? h : (int) (items - 1 - tk[k] * n_heads);
+            if (++h == n_heads) {
+                h = 0;
+                t++;
+            }
+        }
+    }
+    int p[HPW];
+#pragma unroll
+    for (int k = 0; k < HPW; k++) {
+        p[k] = pos ? __ldg(pos + tk[k]) : 0;
+    }
+    float a[HPW][E], b[HPW][E];
+#pragma unroll
+    for (int k = 0; k < HPW; k++) {
+        const ei * s = reinterpret_cast<const ei *>(src) + tk[k] * sts + (int64_t) hd[k] * D + lane * E;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            a[k][e] = io<TI>::to_f(s[e]);
+            b[k][e] = io<TI>::to_f(s[HALF + e]);
+        }
+    }
+    float wa[E], wb[E];
+#pragma unroll
+    for (int e = 0; e < E; e++) {
+        wa[e] = w ? __ldg(w + lane * E + e) : 1.0f;
+        wb[e] = w ? __ldg(w + HALF + lane * E + e) : 1.0f;
+    }
+    float cs[HPW][E], sn[HPW][E];
+    if (rope) {
+#pragma unroll
+        for (int k = 0; k < HPW; k++) {
+            const bool    ok = !pos || (p[k] >= 0 && p[k] < max_pos);
+            const float * c  = rope + (int64_t) (ok ? p[k] : 0) * D + 2 * lane * E;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                cs[k][e] = ok ? __ldg(c + 2 * e) : 0.0f;
+                sn[k][e] = ok ? __ldg(c + 2 * e + 1) : 0.0f;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < HPW; k++) {
+        if (item0 + k >= items) {
+            break;
+        }
+        const int64_t t = tk[k];
+        const int     h = hd[k];
+        if (pos && (p[k] < 0 || p[k] >= max_pos)) {
             if (lane == 0 && err) {
                 atomicOr(err, ACB_DEVERR_POS_RANGE);
             }
-            return;
+            continue;
         }
-    }
-    const ei * s = reinterpret_cast<const ei *>(src) + t * sts + (int64_t) h * D + lane * E;
-    float      a[E], b[E];
+        if (w) {
+            double ss = 0.0;
 #pragma unroll
-    for (int e = 0; e < E; e++) {
-        a[e] = io<TI>::to_f(s[e]);
-        b[e] = io<TI>::to_f(s[HALF + e]);
-    }
-    if (w) {
-        double ss = 0.0;
+            for (int e = 0; e < E; e++) {
+                ss += (double) __fmul_rn(a[k][e], a[k][e]);
+            }
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                ss += (double) __fmul_rn(b[k][e], b[k][e]);
+            }
+            ss             = warp_sum(ss);
+            const float sc = rms_scale(ss, D, eps);
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                a[k][e] = __fmul_rn(__fmul_rn(a[k][e], sc), wa[e]);
+                b[k][e] = __fmul_rn(__fmul_rn(b[k][e], sc), wb[e]);
+            }
+        }
+        eo * d = reinterpret_cast<eo *>(dst) + t * dts + (int64_t) h * dhs + (int64_t) p[k] * dps + lane * E;
+        if (rope) {
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                const float x0 = a[k][e], x1 = b[k][e];
+                a[k][e]        = __fsub_rn(__fmul_rn(x0, cs[k][e]), __fmul_rn(x1, sn[k][e]));
+                b[k][e]        = __fadd_rn(__fmul_rn(x0, sn[k][e]), __fmul_rn(x1, cs[k][e]));
+            }
+        }
 #pragma unroll
         for (int e = 0; e < E; e++) {
-            ss += (double) __fmul_rn(a[e], a[e]);
+            d[e]        = io<TO>::from_f(a[k][e]);
+            d[HALF + e] = io<TO>::from_f(b[k][e]);
         }
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            ss += (double) __fmul_rn(b[e], b[e]);
-        }
-        ss             = warp_sum(ss);
-        const float sc = rms_scale(ss, D, eps);
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * E + e));
-            b[e] = __fmul_rn(__fmul_rn(b[e], sc), __ldg(w + HALF + lane * E + e));
-        }
-    }
-    eo * d = reinterpret_cast<eo *>(dst) + t * dts + (int64_t) h * dhs + (int64_t) p * dps + lane * E;
-    if (rope) {
-        const float * c = rope + (int64_t) p * D + 2 * lane * E;
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            const float cs = __ldg(c + 2 * e), sn = __ldg(c + 2 * e + 1);
-            const float x0 = a[e], x1 = b[e];
-            a[e]           = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-            b[e]           = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-        }
-    }
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        d[e]        = io<TO>::from_f(a[e]);
-        d[HALF + e] = io<TO>::from_f(b[e]);
     }
 }
 
@@ -391,19 +480,21 @@ static acb_status launch_qk(const void * src, int64_t sts, void * dst, int64_t d
                             const float * rope, int max_pos, int * err, cudaStream_t st) {
     const int64_t items = n_tok * n_heads;
     const int     warps = 8;
-    const dim3    grid((unsigned) ((items + warps - 1) / warps));
+    // heads per warp: ~1-2 KB of loads in flight per warp
+    const int     hpw   = D == 64 ? 8 : (D == 128 ? 4 : 2);
+    const dim3    grid((unsigned) ((items + (int64_t) warps * hpw - 1) / ((int64_t) warps * hpw)));
     switch (D) {
         case 64:
-            qk_norm_rope_kernel<TI, TO, 1><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads,
-                                                                       w, eps, pos, rope, max_pos, err);
+            qk_norm_rope_kernel<TI, TO, 1, 8><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
+                                                                          n_heads, w, eps, pos, rope, max_pos, err);
             break;
         case 128:
-            qk_norm_rope_kernel<TI, TO, 2><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads,
-                                                                       w, eps, pos, rope, max_pos, err);
+            qk_norm_rope_kernel<TI, TO, 2, 4><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
+                                                                          n_heads, w, eps, pos, rope, max_pos, err);
             break;
         case 256:
-            qk_norm_rope_kernel<TI, TO, 4><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads,
-                                                                       w, eps, pos, rope, max_pos, err);
+            qk_norm_rope_kernel<TI, TO, 4, 2><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
+                                                                          n_heads, w, eps, pos, rope, max_pos, err);
             break;
         default:
             return ACB_ERR_UNSUPPORTED;
