@@ -1,12 +1,13 @@
 // k_rowops.cu -- row-wise ops of the op-chain: RMSNorm (+weight), adaLN modulate (with the
 // fused RMSNorm), per-head q/k RMSNorm + NeoX RoPE with strided / KV-cache destinations.
 //
-// All three are HBM-bound: one CTA owns one row (a warp for very wide rows; a warp takes a few
-// heads), the row is loaded once with 16-byte vector loads into registers, reduced with
-// shuffles, and written once. The
+// All three are HBM-bound: a CTA owns a row at a time (a warp takes a few heads), the row is
+// loaded once with vector loads into registers, reduced with shuffles, and written once. The
 // sum of squares is accumulated in double (the ggml-CPU rule), which makes the normalisation
 // scale identical to the CPU's; products and sums that ggml performs as separate graph nodes
 // are kept separately rounded (__fmul_rn / __fadd_rn) so no multiply-add is contracted.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace acb {
@@ -228,15 +229,18 @@ static acb_status launch_row_norm(const void * x, int64_t xs, const float * w, v
                                         (reinterpret_cast<uintptr_t>(shift) % 16) == 0 && vs % 4 == 0)) &&
                          (NI * so) >= 8;
     const int nvec = cols / NI;
-    if (aligned && nvec <= 4 * 512) {
-        // a row per CTA at a time, 4 vectors per thread: 32..512 threads; as many CTAs as are
-        // resident at once (per block size, cached)
-        const int threads = ((nvec + 4 * 32 - 1) / (4 * 32)) * 32;
+    // vectors per thread: 4 for f32 rows, 2 for 16-bit rows (8 elements a vector, whose per-column
+    // weight / scale / shift floats would otherwise cost registers and occupancy)
+    constexpr int V = NI == 4 ? 4 : 2;
+    if (aligned && nvec <= V * 512) {
+        // a row per CTA at a time: 32..512 threads; as many CTAs as are resident at once (per
+        // block size, cached)
+        const int threads = ((nvec + V * 32 - 1) / (V * 32)) * 32;
         static int resident[17];
         int &      res = resident[threads / 32];
         if (res == 0) {
             int per_sm = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_norm_cta_kernel<TI, TO, 4, MODE>, threads,
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, row_norm_cta_kernel<TI, TO, V, MODE>, threads,
                                                               0) != cudaSuccess ||
                 per_sm < 1) {
                 per_sm = 1;
@@ -244,7 +248,7 @@ static acb_status launch_row_norm(const void * x, int64_t xs, const float * w, v
             res = per_sm * num_sms();
         }
         const int64_t nb = rows < res ? rows : res;
-        row_norm_cta_kernel<TI, TO, 4, MODE><<<dim3((unsigned) nb), threads, 0, st>>>(x, xs, w, y, ys, rows, cols,
+        row_norm_cta_kernel<TI, TO, V, MODE><<<dim3((unsigned) nb), threads, 0, st>>>(x, xs, w, y, ys, rows, cols,
                                                                                    eps, scale, shift, vs, rps);
     } else {
         row_norm_scalar_kernel<TI, TO, MODE><<<grid, warps * 32, 0, st>>>(x, xs, w, y, ys, rows, cols, eps, scale,
@@ -273,29 +277,74 @@ static acb_status dispatch_row_norm(int ti, int to, const void * x, int64_t xs, 
 }
 
 // ---- per-head q/k RMSNorm + NeoX RoPE ------------------------------------------------------
+// E consecutive elements of an I/O type as floats: one 4-, 8- or 16-byte access when VEC (the
+// caller checked the alignment), else E scalar accesses.
+template <int T, int E, bool VEC> __device__ __forceinline__ void ld_run(const void * p, float * f) {
+    using e         = typename io<T>::t;
+    constexpr int B = E * (int) sizeof(e);
+    if constexpr (VEC && (B == 4 || B == 8 || B == 16)) {
+        using W = std::conditional_t<B == 16, uint4, std::conditional_t<B == 8, uint2, uint32_t>>;
+        union {
+            W u;
+            e v[E];
+        } r;
+        r.u = *reinterpret_cast<const W *>(p);
+#pragma unroll
+        for (int i = 0; i < E; i++) {
+            f[i] = io<T>::to_f(r.v[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < E; i++) {
+            f[i] = io<T>::to_f(reinterpret_cast<const e *>(p)[i]);
+        }
+    }
+}
+
+template <int T, int E, bool VEC> __device__ __forceinline__ void st_run(void * p, const float * f) {
+    using e         = typename io<T>::t;
+    constexpr int B = E * (int) sizeof(e);
+    if constexpr (VEC && (B == 4 || B == 8 || B == 16)) {
+        using W = std::conditional_t<B == 16, uint4, std::conditional_t<B == 8, uint2, uint32_t>>;
+        union {
+            W u;
+            e v[E];
+        } r;
+#pragma unroll
+        for (int i = 0; i < E; i++) {
+            r.v[i] = io<T>::from_f(f[i]);
+        }
+        *reinterpret_cast<W *>(p) = r.u;
+    } else {
+#pragma unroll
+        for (int i = 0; i < E; i++) {
+            reinterpret_cast<e *>(p)[i] = io<T>::from_f(f[i]);
+        }
+    }
+}
+
 // One warp per HPW consecutive (token, head) items. Lane l owns E = D/64 consecutive elements of
 // the first half starting at l*E and the matching elements of the second half, so each NeoX pair
-// (i, i+D/2) lives in one lane. The warp issues the loads of all its heads before any reduction,
-// so a head of 256-512 bytes does not leave the warp waiting on one round trip per head.
-template <int TI, int TO, int E, int HPW>
+// (i, i+D/2) lives in one lane. The warp issues the loads of all its heads (positions, head
+// vectors, norm weights, then the rope rows, which wait only on the positions) before the first
+// use, so a head of 256-512 bytes does not cost a round trip of its own.
+template <int TI, int TO, int E, int HPW, bool VEC>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const void * __restrict__ src, int64_t sts, void * __restrict__ dst, int64_t dts, int64_t dhs, int64_t dps,
     int64_t n_tok, int n_heads, const float * __restrict__ w, float eps, const int32_t * __restrict__ pos,
     const float * __restrict__ rope, int max_pos, int * __restrict__ err) {
-    using ei              = typename io<TI>::t;
-    using eo              = typename io<TO>::t;
-    constexpr int D       = 64 * E;
-    constexpr int HALF    = D / 2;
-    const int     lane    = threadIdx.x & 31;
-    const int64_t items   = n_tok * n_heads;
-    const int64_t item0   = ((int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW;
+    using ei            = typename io<TI>::t;
+    using eo            = typename io<TO>::t;
+    constexpr int D     = 64 * E;
+    constexpr int HALF  = D / 2;
+    const int     lane  = threadIdx.x & 31;
+    const int64_t items = n_tok * n_heads;
+    const int64_t item0 = ((int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * HPW;
     if (item0 >= items) {
         return;
     }
-    // every load of the warp's heads is issued before the first use: positions, the head
-    // vectors, the norm weights, then the rope rows (which wait only on the positions)
-    // (token, head) of each item: one division per warp, then steps of one head (items past the
-    // end are clamped to the last item so that their loads stay in bounds)
+    // (token, head) of each item: one division per warp, then steps of one head; items past the
+    // end repeat the first item so that their loads stay in bounds
     int64_t tk[HPW];
     int     hd[HPW];
     {
@@ -304,8 +353,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 #pragma unroll
         for (int k = 0; k < HPW; k++) {
             const bool in = item0 + k < items;
-            tk[k]         = in ? t : (items - 1) / n_heads;
-            hd[k]         = in ? h : (int) (items - 1 - tk[k] * n_heads);
+            tk[k]         = in ? t : tk[0];
+            hd[k]         = in ? h : hd[0];
             if (++h == n_heads) {
                 h = 0;
                 t++;
@@ -321,17 +370,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 #pragma unroll
     for (int k = 0; k < HPW; k++) {
         const ei * s = reinterpret_cast<const ei *>(src) + tk[k] * sts + (int64_t) hd[k] * D + lane * E;
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            a[k][e] = io<TI>::to_f(s[e]);
-            b[k][e] = io<TI>::to_f(s[HALF + e]);
-        }
+        ld_run<TI, E, VEC>(s, a[k]);
+        ld_run<TI, E, VEC>(s + HALF, b[k]);
     }
     float wa[E], wb[E];
-#pragma unroll
-    for (int e = 0; e < E; e++) {
-        wa[e] = w ? __ldg(w + lane * E + e) : 1.0f;
-        wb[e] = w ? __ldg(w + HALF + lane * E + e) : 1.0f;
+    if (w) {
+        ld_run<ACB_TYPE_F32, E, VEC>(w + lane * E, wa);
+        ld_run<ACB_TYPE_F32, E, VEC>(w + HALF + lane * E, wb);
     }
     float cs[HPW][E], sn[HPW][E];
     if (rope) {
@@ -339,11 +384,49 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
         for (int k = 0; k < HPW; k++) {
             const bool    ok = !pos || (p[k] >= 0 && p[k] < max_pos);
             const float * c  = rope + (int64_t) (ok ? p[k] : 0) * D + 2 * lane * E;
+            float         r[2 * E];
+            if (ok) {
+                ld_run<ACB_TYPE_F32, 2 * E, VEC>(c, r);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 2 * E; e++) {
+                    r[e] = 0.0f;
+                }
+            }
 #pragma unroll
             for (int e = 0; e < E; e++) {
-                cs[k][e] = ok ? __ldg(c + 2 * e) : 0.0f;
-                sn[k][e] = ok ? __ldg(c + 2 * e + 1) : 0.0f;
+                cs[k][e] = r[2 * e];
+                sn[k][e] = r[2 * e + 1];
             }
+        }
+    }
+    // the heads' sums of squares are reduced side by side (same butterfly per head), so their
+    // shuffle and division latencies overlap instead of adding up
+    float sc[HPW];
+    if (w) {
+        double ss[HPW];
+#pragma unroll
+        for (int k = 0; k < HPW; k++) {
+            ss[k] = 0.0;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                ss[k] += (double) __fmul_rn(a[k][e], a[k][e]);
+            }
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                ss[k] += (double) __fmul_rn(b[k][e], b[k][e]);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int k = 0; k < HPW; k++) {
+                ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], o);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < HPW; k++) {
+            sc[k] = rms_scale(ss[k], D, eps);
         }
     }
 #pragma unroll
@@ -351,8 +434,6 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
         if (item0 + k >= items) {
             break;
         }
-        const int64_t t = tk[k];
-        const int     h = hd[k];
         if (pos && (p[k] < 0 || p[k] >= max_pos)) {
             if (lane == 0 && err) {
                 atomicOr(err, ACB_DEVERR_POS_RANGE);
@@ -360,24 +441,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
             continue;
         }
         if (w) {
-            double ss = 0.0;
 #pragma unroll
             for (int e = 0; e < E; e++) {
-                ss += (double) __fmul_rn(a[k][e], a[k][e]);
-            }
-#pragma unroll
-            for (int e = 0; e < E; e++) {
-                ss += (double) __fmul_rn(b[k][e], b[k][e]);
-            }
-            ss             = warp_sum(ss);
-            const float sc = rms_scale(ss, D, eps);
-#pragma unroll
-            for (int e = 0; e < E; e++) {
-                a[k][e] = __fmul_rn(__fmul_rn(a[k][e], sc), wa[e]);
-                b[k][e] = __fmul_rn(__fmul_rn(b[k][e], sc), wb[e]);
+                a[k][e] = __fmul_rn(__fmul_rn(a[k][e], sc[k]), wa[e]);
+                b[k][e] = __fmul_rn(__fmul_rn(b[k][e], sc[k]), wb[e]);
             }
         }
-        eo * d = reinterpret_cast<eo *>(dst) + t * dts + (int64_t) h * dhs + (int64_t) p[k] * dps + lane * E;
         if (rope) {
 #pragma unroll
             for (int e = 0; e < E; e++) {
@@ -386,11 +455,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
                 b[k][e]        = __fadd_rn(__fmul_rn(x0, sn[k][e]), __fmul_rn(x1, cs[k][e]));
             }
         }
-#pragma unroll
-        for (int e = 0; e < E; e++) {
-            d[e]        = io<TO>::from_f(a[k][e]);
-            d[HALF + e] = io<TO>::from_f(b[k][e]);
-        }
+        eo * d = reinterpret_cast<eo *>(dst) + tk[k] * dts + (int64_t) hd[k] * dhs + (int64_t) p[k] * dps + lane * E;
+        st_run<TO, E, VEC>(d, a[k]);
+        st_run<TO, E, VEC>(d + HALF, b[k]);
     }
 }
 
@@ -474,30 +541,51 @@ __global__ void __launch_bounds__(256) qk_planes_kernel(const void * __restrict_
     *reinterpret_cast<__half2 *>(d + lo_off + 64) = bl;
 }
 
+template <int TI, int TO, int E, int HPW>
+static void launch_qk_e(bool vec, dim3 grid, const void * src, int64_t sts, void * dst, int64_t dts, int64_t dhs,
+                        int64_t dps, int64_t n_tok, int n_heads, const float * w, float eps, const int32_t * pos,
+                        const float * rope, int max_pos, int * err, cudaStream_t st) {
+    if constexpr (E > 1) {  // a single element per lane has nothing to vectorise
+        if (vec) {
+            qk_norm_rope_kernel<TI, TO, E, HPW, true><<<grid, 256, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
+                                                                            n_heads, w, eps, pos, rope, max_pos, err);
+            return;
+        }
+    }
+    qk_norm_rope_kernel<TI, TO, E, HPW, false>
+        <<<grid, 256, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok, n_heads, w, eps, pos, rope, max_pos, err);
+}
+
 template <int TI, int TO>
 static acb_status launch_qk(const void * src, int64_t sts, void * dst, int64_t dts, int64_t dhs, int64_t dps,
                             int64_t n_tok, int n_heads, int D, const float * w, float eps, const int32_t * pos,
                             const float * rope, int max_pos, int * err, cudaStream_t st) {
+    if (D != 64 && D != 128 && D != 256) {
+        return ACB_ERR_UNSUPPORTED;
+    }
     const int64_t items = n_tok * n_heads;
-    const int     warps = 8;
-    // heads per warp: ~1-2 KB of loads in flight per warp
-    const int     hpw   = D == 64 ? 8 : (D == 128 ? 4 : 2);
-    const dim3    grid((unsigned) ((items + (int64_t) warps * hpw - 1) / ((int64_t) warps * hpw)));
+    // heads per warp: 0.5-2 KB of loads in flight per warp; 8 warps per CTA
+    const int  hpw = D == 256 ? 2 : 4;
+    const dim3 grid((unsigned) ((items + 8LL * hpw - 1) / (8LL * hpw)));
+    // each lane's E = D/64 consecutive elements as one access when every run is aligned to its size
+    const int  E  = D / 64;
+    const int  si = (int) sizeof(typename io<TI>::t), so = (int) sizeof(typename io<TO>::t);
+    auto       al = [](const void * q, int b) { return (reinterpret_cast<uintptr_t>(q) % (uintptr_t) b) == 0; };
+    const bool vec = E > 1 && al(src, E * si) && al(dst, E * so) && sts % E == 0 && dts % E == 0 && dhs % E == 0 &&
+                     dps % E == 0 && (!w || al(w, E * 4)) && (!rope || al(rope, 2 * E * 4));
     switch (D) {
         case 64:
-            qk_norm_rope_kernel<TI, TO, 1, 8><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
-                                                                          n_heads, w, eps, pos, rope, max_pos, err);
+            launch_qk_e<TI, TO, 1, 4>(false, grid, src, sts, dst, dts, dhs, dps, n_tok, n_heads, w, eps, pos, rope,
+                                      max_pos, err, st);
             break;
         case 128:
-            qk_norm_rope_kernel<TI, TO, 2, 4><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
-                                                                          n_heads, w, eps, pos, rope, max_pos, err);
-            break;
-        case 256:
-            qk_norm_rope_kernel<TI, TO, 4, 2><<<grid, warps * 32, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
-                                                                          n_heads, w, eps, pos, rope, max_pos, err);
+            launch_qk_e<TI, TO, 2, 4>(vec, grid, src, sts, dst, dts, dhs, dps, n_tok, n_heads, w, eps, pos, rope,
+                                      max_pos, err, st);
             break;
         default:
-            return ACB_ERR_UNSUPPORTED;
+            launch_qk_e<TI, TO, 4, 2>(vec, grid, src, sts, dst, dts, dhs, dps, n_tok, n_heads, w, eps, pos, rope,
+                                      max_pos, err, st);
+            break;
     }
     return launch_status();
 }
