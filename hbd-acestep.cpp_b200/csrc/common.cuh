@@ -115,6 +115,15 @@ __device__ __forceinline__ float rms_scale(double sumsq, int n, float eps) {
     return 1.0f / sqrtf(__fadd_rn(mean, eps));
 }
 
+// rms_scale for a power-of-two count NN: the mean is sumsq * 2^-k, which equals sumsq / NN
+// exactly in double (a power-of-two scaling of a sum of float squares stays normal), so the scale
+// is bit-identical to rms_scale's without a double division (per-head norms run it in every lane).
+template <int NN> __device__ __forceinline__ float rms_scale_pow2(double sumsq, float eps) {
+    static_assert(NN > 0 && (NN & (NN - 1)) == 0, "power of two");
+    const float mean = (float) (sumsq * (1.0 / (double) NN));
+    return 1.0f / sqrtf(__fadd_rn(mean, eps));
+}
+
 __device__ __forceinline__ uint16_t ld_u16(const uint8_t * p) {
     return (uint16_t) (p[0] | (p[1] << 8));
 }

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(const float * __restrict_
                 ss += (double) __fmul_rn(b[e], b[e]);
             }
             ss             = warp_sum(ss);
-            const float sc = rms_scale(ss, D, eps);
+            const float sc = rms_scale_pow2<D>(ss, eps);
 #pragma unroll
             for (int e = 0; e < E; e++) {
                 a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * E + e));

@@ -652,7 +652,7 @@ __device__ __forceinline__ void pd_norm_rope(const float * src, const float * w,
             ss += (double) __fmul_rn(b[e], b[e]);
         }
         ss             = warp_sum(ss);
-        const float sc = rms_scale(ss, kPdD, eps);
+        const float sc = rms_scale_pow2<kPdD>(ss, eps);
 #pragma unroll
         for (int e = 0; e < 2; e++) {
             a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * 2 + e));

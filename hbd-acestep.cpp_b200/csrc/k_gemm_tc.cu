@@ -332,7 +332,7 @@ __device__ __forceinline__ void qkv_epilogue(const GemmArgs & g, uint32_t tacc, 
                         t[l] = t[l] + t[l + o];
                     }
                 }
-                sc = rms_scale(t[0], 128, g.eps);
+                sc = rms_scale_pow2<128>(t[0], g.eps);
             }
 #pragma unroll 1
             for (int c = 0; c < 2; c++) {

@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
         }
 #pragma unroll
         for (int k = 0; k < HPW; k++) {
-            sc[k] = rms_scale(ss[k], D, eps);
+            sc[k] = rms_scale_pow2<D>(ss[k], eps);
         }
     }
 #pragma unroll
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(256) qk_planes_kernel(const void * __restrict_
         ss += (double) __fmul_rn(b[0], b[0]);
         ss += (double) __fmul_rn(b[1], b[1]);
         ss             = warp_sum(ss);
-        const float sc = rms_scale(ss, 128, eps);
+        const float sc = rms_scale_pow2<128>(ss, eps);
 #pragma unroll
         for (int e = 0; e < 2; e++) {
             a[e] = __fmul_rn(__fmul_rn(a[e], sc), __ldg(w + lane * 2 + e));
