@@ -74,6 +74,39 @@ template <> __device__ __forceinline__ float deq<ACB_TYPE_Q6_K>(const uint8_t * 
     return __fmul_rn(ds, (float) q);
 }
 
+// Dequantise the NO consecutive elements v*NO .. v*NO+NO-1 of a row held in shared memory.
+template <int QT, int NO> __device__ __forceinline__ void deq_vec(const uint8_t * row, int v, float * f) {
+#pragma unroll
+    for (int j = 0; j < NO; j++) {
+        f[j] = deq<QT>(row, v * NO + j);
+    }
+}
+
+// Q8_0: the NO elements share one block (NO divides 32); its f16 scale is one 2-byte load and
+// the int8 quants NO/2 2-byte loads (a block starts at an even offset, 34 bytes per block).
+template <> __device__ __forceinline__ void deq_vec<ACB_TYPE_Q8_0, 4>(const uint8_t * row, int v, float * f) {
+    const uint8_t * b = row + (v >> 3) * 34;
+    const float     d = f16_bits_to_f(*reinterpret_cast<const uint16_t *>(b));
+    const uint16_t * q = reinterpret_cast<const uint16_t *>(b + 2 + (v & 7) * 4);
+    const uint16_t  q0 = q[0], q1 = q[1];
+    f[0]               = __fmul_rn(d, (float) (int8_t) (q0 & 0xff));
+    f[1]               = __fmul_rn(d, (float) (int8_t) (q0 >> 8));
+    f[2]               = __fmul_rn(d, (float) (int8_t) (q1 & 0xff));
+    f[3]               = __fmul_rn(d, (float) (int8_t) (q1 >> 8));
+}
+
+template <> __device__ __forceinline__ void deq_vec<ACB_TYPE_Q8_0, 8>(const uint8_t * row, int v, float * f) {
+    const uint8_t * b = row + (v >> 2) * 34;
+    const float     d = f16_bits_to_f(*reinterpret_cast<const uint16_t *>(b));
+    const uint16_t * q = reinterpret_cast<const uint16_t *>(b + 2 + (v & 3) * 8);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint16_t w = q[j];
+        f[2 * j]         = __fmul_rn(d, (float) (int8_t) (w & 0xff));
+        f[2 * j + 1]     = __fmul_rn(d, (float) (int8_t) (w >> 8));
+    }
+}
+
 template <int QT, int TO>
 __global__ void __launch_bounds__(256) get_rows_q_kernel(const uint8_t * __restrict__ table, int64_t n_rows,
                                                          int64_t row_bytes, int cols, const int32_t * __restrict__ ids,
@@ -121,9 +154,11 @@ __global__ void __launch_bounds__(256) get_rows_q_kernel(const uint8_t * __restr
             eo    e[NO];
             uint4 u;
         } r;
+        float f[NO];
+        deq_vec<QT, NO>(srow, v, f);
 #pragma unroll
         for (int j = 0; j < NO; j++) {
-            r.e[j] = io<TO>::from_f(deq<QT>(srow, v * NO + j));
+            r.e[j] = io<TO>::from_f(f[j]);
         }
         __stcs(reinterpret_cast<uint4 *>(orow) + v, r.u);
     }
