@@ -8,8 +8,16 @@
 
 namespace acb {
 
-template <int T> __device__ __forceinline__ float silu_mul(float g, float u) {
-    return silu_times(g, u);
+// silu(g) * u for an output of type TO. A bf16 output keeps 8 mantissa bits, so the fast exp and
+// divide intrinsics (a few f32 ulps) round to the same bf16 value as g / (1 + expf(-g)) except
+// within a few ulps of a rounding boundary (then one bf16 step apart); they take the kernel from
+// issue-bound to HBM-bound. Other outputs keep the correctly rounded chain.
+template <int TO> __device__ __forceinline__ float silu_mul(float g, float u) {
+    if constexpr (TO == ACB_TYPE_BF16) {
+        return __fmul_rn(__fdividef(g, __fadd_rn(1.0f, __expf(-g))), u);
+    } else {
+        return silu_times(g, u);
+    }
 }
 
 template <int TI, int TO, int U>
@@ -45,7 +53,7 @@ __global__ void __launch_bounds__(256) swiglu_vec_kernel(const void * __restrict
                 } res;
 #pragma unroll
                 for (int j = 0; j < N; j++) {
-                    res.e[j] = io<TO>::from_f(silu_mul<0>(gv[k].get(j), uv[k].get(j)));
+                    res.e[j] = io<TO>::from_f(silu_mul<TO>(gv[k].get(j), uv[k].get(j)));
                 }
                 eo * dst = o + vi * N;
                 if constexpr (N * sizeof(eo) == 8) {
