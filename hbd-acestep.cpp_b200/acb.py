@@ -116,6 +116,7 @@ def lib():
             "acb_dit_eval": (I, [P, P, P, P, P]),
             "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
             "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
+            "acb_dit_dpm3m": (I, [P, P, P, P, I, P, I64, P]),
             "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_norm_quant": (I, [P, I64, I64, I64, P, F, P, P, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_qk_norm_rope_planes": (I, [P, I, I64, P, I64, I64, I64, I, P, I, P, I, F, P, P, I, P, P]),
@@ -758,6 +759,14 @@ def dit_euler(xt, vt, tt3, last, out=None, stream=None):
     _check("acb_dit_euler", lib().acb_dit_euler(_ptr(xt), _ptr(vt), _ptr(tt3), int(last), _ptr(out), xt.numel(),
                                                 _stream(stream)))
     return out
+
+
+def dit_dpm3m(xt, vt, prev_vt, prev_prev_vt, history, tt3, stream=None):
+    """DPM++ 3M step in place: xt advances from tt3[0] to tt3[2] with the velocity history
+    (history = stored velocities, 0..2), then prev_prev_vt <- prev_vt and prev_vt <- vt."""
+    _check("acb_dit_dpm3m", lib().acb_dit_dpm3m(_ptr(xt), _ptr(vt), _ptr(prev_vt), _ptr(prev_prev_vt), int(history),
+                                                _ptr(tt3), xt.numel(), _stream(stream)))
+    return xt
 
 
 def attn_vt(v, Nkv, lo=False, vt_ld=None, out=None, stream=None):

@@ -147,6 +147,32 @@ __global__ void dit_euler_kernel(float * __restrict__ xt, const float * __restri
     }
 }
 
+// DPM++ 3M step (src/solvers/solver-dpm.h:14-50): a third-order Adams-Bashforth step on the
+// velocity with two stored velocities, second order with one, Euler with none; then the history
+// moves down (prev_prev <- prev, prev <- vt). Every element is independent, so the shift happens
+// in place in the same pass. Products and sums are rounded one by one in the reference's order.
+__global__ void dit_dpm3m_kernel(float * __restrict__ xt, const float * __restrict__ vt, float * __restrict__ prev,
+                                 float * __restrict__ prev_prev, int history, const float * __restrict__ tt,
+                                 int64_t n) {
+    const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) {
+        return;
+    }
+    constexpr float c0 = 23.0f / 12.0f, c1 = 16.0f / 12.0f, c2 = 5.0f / 12.0f;
+    const float     dt = __fsub_rn(tt[0], tt[2]);
+    const float     v  = vt[i];
+    float           ve = v;
+    const float     p1 = prev[i];
+    if (history >= 2) {
+        ve = __fadd_rn(__fsub_rn(__fmul_rn(c0, v), __fmul_rn(c1, p1)), __fmul_rn(c2, prev_prev[i]));
+    } else if (history == 1) {
+        ve = __fsub_rn(__fmul_rn(1.5f, v), __fmul_rn(0.5f, p1));
+    }
+    xt[i]        = __fsub_rn(xt[i], __fmul_rn(ve, dt));
+    prev_prev[i] = p1;
+    prev[i]      = v;
+}
+
 }  // namespace acb
 
 using namespace acb;
@@ -217,5 +243,18 @@ extern "C" acb_status acb_dit_euler(float * xt, const float * vt, const float * 
         return ACB_OK;
     }
     dit_euler_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(xt, vt, tt, last, out, n);
+    return launch_status();
+}
+
+extern "C" acb_status acb_dit_dpm3m(float * xt, const float * vt, float * prev_vt, float * prev_prev_vt, int history,
+                                    const float * tt, int64_t n, acb_stream_t stream) {
+    if (!xt || !vt || !prev_vt || !prev_prev_vt || !tt || history < 0 || n < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (n == 0) {
+        return ACB_OK;
+    }
+    dit_dpm3m_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(xt, vt, prev_vt, prev_prev_vt, history,
+                                                                             tt, n);
     return launch_status();
 }

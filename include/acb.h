@@ -356,6 +356,14 @@ ACB_API acb_status acb_dit_apg(const float * cond, const float * uncond, double 
  * out = xt - vt * t_curr (the x0 prediction, dit-sampler.h:596-604). */
 ACB_API acb_status acb_dit_euler(float * xt, const float * vt, const float * tt, int last, float * out, int64_t n,
                                  acb_stream_t stream);
+/* DPM++ 3M step, the "dpm3m" solver (src/solvers/solver-dpm.h:14-50; registry solver-registry.h:32):
+ * tt = {t_curr, t_r, t_next}, dt = t_curr - t_next; history = velocities stored so far, capped at 2
+ * (the step index for steps 0, 1, then 2). history 0: xt -= vt*dt; 1: xt -= (1.5 vt - 0.5 prev)*dt;
+ * 2: xt -= (23/12 vt - 16/12 prev + 5/12 prev_prev)*dt. Then prev_prev_vt <- prev_vt and prev_vt <- vt,
+ * in place (both [n] f32, caller-owned; their contents are ignored while history says they are
+ * empty). The last step of a schedule is acb_dit_euler with last != 0, as for every solver. */
+ACB_API acb_status acb_dit_dpm3m(float * xt, const float * vt, float * prev_vt, float * prev_prev_vt, int history,
+                                 const float * tt, int64_t n, acb_stream_t stream);
 
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 

@@ -585,3 +585,23 @@ def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, mo
         dt = np.float32(np.float32(t) - np.float32(schedule[step + 1]))
         xt = (xt - v * dt).astype(np.float32)
     return xt
+
+
+def dpm3m_step(xt, vt, prev_vt, prev_prev_vt, t_curr, t_next):
+    """One DPM++ 3M step (src/solvers/solver-dpm.h:14-50), in float32 with every product and sum
+    rounded in the reference's source order: third-order Adams-Bashforth with two stored
+    velocities, second order with one (prev_prev_vt None), Euler with none (prev_vt None).
+    Returns (xt, prev_vt, prev_prev_vt) after the step: the history moves down by one."""
+    f = np.float32
+    vt = np.asarray(vt, dtype=np.float32)
+    dt = f(f(t_curr) - f(t_next))
+    if prev_vt is not None and prev_prev_vt is not None:
+        c0, c1, c2 = f(23.0) / f(12.0), f(16.0) / f(12.0), f(5.0) / f(12.0)
+        v = ((c0 * vt).astype(np.float32) - (c1 * prev_vt).astype(np.float32)).astype(np.float32)
+        v = (v + (c2 * prev_prev_vt).astype(np.float32)).astype(np.float32)
+    elif prev_vt is not None:
+        v = ((f(1.5) * vt).astype(np.float32) - (f(0.5) * prev_vt).astype(np.float32)).astype(np.float32)
+    else:
+        v = vt
+    xt = (np.asarray(xt, dtype=np.float32) - (v * dt).astype(np.float32)).astype(np.float32)
+    return xt, vt.copy(), (None if prev_vt is None else np.asarray(prev_vt, dtype=np.float32).copy())

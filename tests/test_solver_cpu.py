@@ -1,0 +1,58 @@
+"""CPU: pin the oracle's DPM++ 3M step (src/solvers/solver-dpm.h:14-50) by properties that do not
+restate its formula: the Adams-Bashforth weights of each order sum to one (a constant velocity
+field moves xt exactly like Euler), third order integrates a velocity that is quadratic in t
+exactly over uniform steps, second order a linear one, and the history moves down one slot per
+step with the reference's bootstrap (Euler, then second, then third order)."""
+import numpy as np
+
+import oracle as O
+
+
+def _run(v_of_t, ts, x0):
+    x, p, pp = x0.astype(np.float32), None, None
+    for a, b in zip(ts[:-1], ts[1:]):
+        x, p, pp = O.dpm3m_step(x, v_of_t(a), p, pp, a, b)
+    return x, p, pp
+
+
+def test_dpm3m_constant_velocity_moves_like_euler():
+    rng = np.random.default_rng(1)
+    v = rng.standard_normal(1000).astype(np.float32)
+    x0 = rng.standard_normal(1000).astype(np.float32)
+    ts = np.linspace(1.0, 0.25, 7)
+    x, _, _ = _run(lambda t: v, ts, x0)
+    want = x0.astype(np.float64) - v.astype(np.float64) * (ts[0] - ts[-1])
+    assert np.abs(x - want).max() <= 1e-5 * (np.abs(want).max() + 1)
+
+
+def test_dpm3m_orders_are_exact_on_polynomials():
+    # after the bootstrap, a step of order k integrates v(t) of degree k-1 exactly (uniform steps)
+    h = 0.125
+    ts = 1.0 - h * np.arange(6)
+    a, b, c = 0.7, -1.3, 2.1
+    quad = lambda t: np.array([a + b * t + c * t * t], dtype=np.float32)
+    integral = lambda t0, t1: a * (t0 - t1) + b * (t0 ** 2 - t1 ** 2) / 2 + c * (t0 ** 3 - t1 ** 3) / 3
+    x = np.zeros(1, np.float32)
+    p = pp = None
+    for i in range(5):
+        t0, t1 = ts[i], ts[i + 1]
+        xb = x.astype(np.float64)
+        x, p, pp = O.dpm3m_step(x, quad(t0), p, pp, t0, t1)
+        if i >= 2:  # third order from the third step on
+            assert abs(float(x[0]) - (xb[0] - integral(t0, t1))) <= 2e-6
+    lin = lambda t: np.array([a + b * t], dtype=np.float32)
+    x1, p1, _ = O.dpm3m_step(np.zeros(1, np.float32), lin(ts[0]), None, None, ts[0], ts[1])
+    x2, _, _ = O.dpm3m_step(x1, lin(ts[1]), p1, None, ts[1], ts[2])
+    want = -(a * (ts[1] - ts[2]) + b * (ts[1] ** 2 - ts[2] ** 2) / 2)
+    assert abs(float(x2[0] - x1[0]) - want) <= 1e-6
+
+
+def test_dpm3m_history_shift():
+    v0, v1, v2 = (np.full(3, k, np.float32) for k in (1.0, 2.0, 3.0))
+    x = np.zeros(3, np.float32)
+    x, p, pp = O.dpm3m_step(x, v0, None, None, 1.0, 0.5)
+    assert pp is None and np.array_equal(p, v0) and np.array_equal(x, -0.5 * v0)
+    x, p, pp = O.dpm3m_step(x, v1, p, pp, 0.5, 0.25)
+    assert np.array_equal(p, v1) and np.array_equal(pp, v0)
+    x, p, pp = O.dpm3m_step(x, v2, p, pp, 0.25, 0.125)
+    assert np.array_equal(p, v2) and np.array_equal(pp, v1)
