@@ -117,6 +117,7 @@ def lib():
             "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
             "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
             "acb_dit_dpm3m": (I, [P, P, P, P, I, P, I64, P]),
+            "acb_dit_sde": (I, [P, P, P, P, I64, P]),
             "acb_act_quant_ex": (I, [P, I64, I64, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_norm_quant": (I, [P, I64, I64, I64, P, F, P, P, I64, I64, I, I, P, I, I64, I64, P]),
             "acb_qk_norm_rope_planes": (I, [P, I, I64, P, I64, I64, I64, I, P, I, P, I, F, P, P, I, P, P]),
@@ -766,6 +767,12 @@ def dit_dpm3m(xt, vt, prev_vt, prev_prev_vt, history, tt3, stream=None):
     (history = stored velocities, 0..2), then prev_prev_vt <- prev_vt and prev_vt <- vt."""
     _check("acb_dit_dpm3m", lib().acb_dit_dpm3m(_ptr(xt), _ptr(vt), _ptr(prev_vt), _ptr(prev_prev_vt), int(history),
                                                 _ptr(tt3), xt.numel(), _stream(stream)))
+    return xt
+
+
+def dit_sde(xt, vt, noise, tt3, stream=None):
+    """SDE ancestral step in place: x0 = xt - vt * tt3[0], then xt = tt3[2] * noise + (1 - tt3[2]) * x0."""
+    _check("acb_dit_sde", lib().acb_dit_sde(_ptr(xt), _ptr(vt), _ptr(noise), _ptr(tt3), xt.numel(), _stream(stream)))
     return xt
 
 

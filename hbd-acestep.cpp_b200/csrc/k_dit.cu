@@ -173,6 +173,20 @@ __global__ void dit_dpm3m_kernel(float * __restrict__ xt, const float * __restri
     prev[i]      = v;
 }
 
+// SDE ancestral step (src/solvers/solver-sde.h:17-38): predict x0 = xt - vt * t_curr, then renoise
+// to the next time, xt = t_next * noise + (1 - t_next) * x0, each product and sum rounded in the
+// reference's order. The noise is an input (the reference draws it per batch item on the host).
+__global__ void dit_sde_kernel(float * __restrict__ xt, const float * __restrict__ vt,
+                               const float * __restrict__ noise, const float * __restrict__ tt, int64_t n) {
+    const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) {
+        return;
+    }
+    const float t_curr = tt[0], t_next = tt[2];
+    const float x0     = __fsub_rn(xt[i], __fmul_rn(vt[i], t_curr));
+    xt[i]              = __fadd_rn(__fmul_rn(t_next, noise[i]), __fmul_rn(__fsub_rn(1.0f, t_next), x0));
+}
+
 }  // namespace acb
 
 using namespace acb;
@@ -256,5 +270,17 @@ extern "C" acb_status acb_dit_dpm3m(float * xt, const float * vt, float * prev_v
     }
     dit_dpm3m_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(xt, vt, prev_vt, prev_prev_vt, history,
                                                                              tt, n);
+    return launch_status();
+}
+
+extern "C" acb_status acb_dit_sde(float * xt, const float * vt, const float * noise, const float * tt, int64_t n,
+                                  acb_stream_t stream) {
+    if (!xt || !vt || !noise || !tt || n < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (n == 0) {
+        return ACB_OK;
+    }
+    dit_sde_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(xt, vt, noise, tt, n);
     return launch_status();
 }

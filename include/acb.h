@@ -364,6 +364,13 @@ ACB_API acb_status acb_dit_euler(float * xt, const float * vt, const float * tt,
  * empty). The last step of a schedule is acb_dit_euler with last != 0, as for every solver. */
 ACB_API acb_status acb_dit_dpm3m(float * xt, const float * vt, float * prev_vt, float * prev_prev_vt, int history,
                                  const float * tt, int64_t n, acb_stream_t stream);
+/* SDE ancestral step, the "sde" solver (src/solvers/solver-sde.h:17-38): tt = {t_curr, t_r, t_next};
+ * xt = t_next * noise + (1 - t_next) * (xt - vt * t_curr). noise [n] f32 is the caller's: the
+ * reference draws, for batch item b at step s, N(0,1) from Philox seeded with seed_b + s + 1 and
+ * rounds it to bf16 (philox.h:113-126, the values torch.randn gives in bf16 on a CUDA generator
+ * with that seed). The last step of a schedule is acb_dit_euler with last != 0. */
+ACB_API acb_status acb_dit_sde(float * xt, const float * vt, const float * noise, const float * tt, int64_t n,
+                               acb_stream_t stream);
 
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 

@@ -605,3 +605,14 @@ def dpm3m_step(xt, vt, prev_vt, prev_prev_vt, t_curr, t_next):
         v = vt
     xt = (np.asarray(xt, dtype=np.float32) - (v * dt).astype(np.float32)).astype(np.float32)
     return xt, vt.copy(), (None if prev_vt is None else np.asarray(prev_vt, dtype=np.float32).copy())
+
+
+def sde_step(xt, vt, noise, t_curr, t_next):
+    """One SDE ancestral step (src/solvers/solver-sde.h:17-38) in float32, rounded in the
+    reference's order: x0 = xt - vt * t_curr; xt = t_next * noise + (1 - t_next) * x0. The noise
+    (Philox N(0,1) rounded to bf16 in the reference) is an input."""
+    f = np.float32
+    x0 = (np.asarray(xt, np.float32) - (np.asarray(vt, np.float32) * f(t_curr)).astype(np.float32)).astype(np.float32)
+    a = (f(t_next) * np.asarray(noise, np.float32)).astype(np.float32)
+    b = ((f(1.0) - f(t_next)) * x0).astype(np.float32)
+    return (a + b).astype(np.float32)

@@ -56,3 +56,12 @@ def test_dpm3m_history_shift():
     assert np.array_equal(p, v1) and np.array_equal(pp, v0)
     x, p, pp = O.dpm3m_step(x, v2, p, pp, 0.25, 0.125)
     assert np.array_equal(p, v2) and np.array_equal(pp, v1)
+
+
+def test_sde_step_endpoints():
+    # t_next = 0 gives the x0 prediction itself; t_next = 1 gives pure noise
+    rng = np.random.default_rng(5)
+    x, v, z = (rng.standard_normal(64).astype(np.float32) for _ in range(3))
+    x0 = (x - (v * np.float32(0.7)).astype(np.float32)).astype(np.float32)
+    assert np.array_equal(O.sde_step(x, v, z, 0.7, 0.0), x0)
+    assert np.array_equal(O.sde_step(x, v, z, 0.7, 1.0), z)
