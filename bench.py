@@ -1070,7 +1070,7 @@ def run_dit(dev, rank, want_cpu=True, reps=2, modes=("exact", "fast")):
                          "traffic": None},
             "e2e": {"value": round(DIT_STEPS / e2e_s, 3), "unit": "step/s",
                     "h2d_bytes_per_step": (noise.nbytes + ctx.nbytes + enc.nbytes) // DIT_STEPS,
-                    "d2h_bytes_per_step": x0.nbytes // DIT_STEPS, "path": "acb_dit_generate (host arrays)"},
+                    "d2h_bytes_per_step": x0.nbytes // DIT_STEPS, "path": "acb_dit_generate_solver (host arrays, Euler)"},
         }
     res["value"] = res[modes[0]]["value"]
     if want_cpu:

@@ -107,6 +107,7 @@ def lib():
             "acb_dit_set_exact": (I, [P, I]),
             "acb_dit_forward": (I, [P, P, P, I, I, I, F, F, P, I, P]),
             "acb_dit_generate": (I, [P, P, P, P, I, I, I, I, P, P, F, P]),
+            "acb_dit_generate_solver": (I, [P, P, P, P, I, I, I, I, P, P, F, I, P]),
             "acb_dit_free": (None, [P]),
             "acb_dit_set_condition": (I, [P, P, I, I, I, P]),
             "acb_attn_tc": (I, [P, I64, P, I64, P, I64, P, I, I64, I, I, I, I, I, I, I, I, I, F, I, I64, I64, I64, P,
@@ -719,9 +720,11 @@ class DiT:
         _check("acb_dit_eval", lib().acb_dit_eval(self.h, _ptr(x), _ptr(tt), _ptr(out), _stream(stream)))
         return out
 
-    def generate(self, noise, context, enc, schedule, guidance_scale=1.0):
+    SOLVERS = {"euler": 0, "dpm3m": 1}
+
+    def generate(self, noise, context, enc, schedule, guidance_scale=1.0, solver="euler"):
         """Host arrays: noise [N, T, Oc], context [N, T, in-Oc], enc [N, enc_S, enc_hidden] ->
-        (x0 [N, T, Oc], device ms of the step loop)."""
+        (x0 [N, T, Oc], device ms of the step loop). solver: "euler" or "dpm3m"."""
         np = self.np
         noise = np.ascontiguousarray(noise, dtype=np.float32)
         context = np.ascontiguousarray(context, dtype=np.float32)
@@ -730,9 +733,10 @@ class DiT:
         N, T, _ = noise.shape
         out = np.empty_like(noise)
         ms = C.c_float(0.0)
-        _check("acb_dit_generate", lib().acb_dit_generate(
+        _check("acb_dit_generate_solver", lib().acb_dit_generate_solver(
             self.h, noise.ctypes.data, context.ctypes.data, enc.ctypes.data, enc.shape[1], T, N, sched.size,
-            sched.ctypes.data, out.ctypes.data, float(guidance_scale), C.cast(C.pointer(ms), C.c_void_p)))
+            sched.ctypes.data, out.ctypes.data, float(guidance_scale), self.SOLVERS[solver],
+            C.cast(C.pointer(ms), C.c_void_p)))
         return out, ms.value
 
 

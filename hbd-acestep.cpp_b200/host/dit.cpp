@@ -78,6 +78,7 @@ struct acb_dit {
     int    eval_kernels   = 0;            // kernel launches of one captured evaluation
     // generate
     DevBuf                          xt, vt, out, ra;
+    DevBuf                          hist1, hist2;  // DPM++ 3M velocity history (previous, the one before)
     std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
 
     ~acb_dit() {
@@ -819,10 +820,19 @@ extern "C" acb_status acb_dit_eval(acb_dit * m, const float * d_input, const flo
 extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
                                        const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                        const float * schedule, float * output, float guidance_scale, float * gpu_ms) {
+    return acb_dit_generate_solver(m, noise, context_latents, enc_hidden, enc_S, T, N, num_steps, schedule, output,
+                                   guidance_scale, ACB_SOLVER_EULER, gpu_ms);
+}
+
+extern "C" acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, const float * context_latents,
+                                              const float * enc_hidden, int enc_S, int T, int N, int num_steps,
+                                              const float * schedule, float * output, float guidance_scale,
+                                              int solver, float * gpu_ms) {
     if (!m || !noise || !context_latents || !enc_hidden || !schedule || !output || N <= 0 || T <= 0 || enc_S <= 0 ||
-        num_steps <= 0 || T % m->c.patch_size != 0) {
+        num_steps <= 0 || T % m->c.patch_size != 0 || (solver != ACB_SOLVER_EULER && solver != ACB_SOLVER_DPM3M)) {
         return ACB_ERR_INVALID_ARG;
     }
+    const bool dpm = solver == ACB_SOLVER_DPM3M;
     if (cudaSetDevice(m->device) != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
@@ -837,11 +847,12 @@ extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const f
     cudaStream_t s     = m->st;
     const size_t n_per = (size_t) T * Oc, n_tot = n_per * N;
     bool         bad   = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
-                 m->ra.bytes < n_tot * 8;
+                 m->ra.bytes < n_tot * 8 || (dpm && (m->hist1.bytes < n_tot * 4 || m->hist2.bytes < n_tot * 4));
     if (bad) {
         m->drop_graphs();  // the graphs hold these addresses
         if (m->xt.alloc(n_tot * 4) != ACB_OK || m->vt.alloc(n_tot * 4) != ACB_OK || m->out.alloc(n_tot * 4) != ACB_OK ||
-            m->ra.alloc(n_tot * 8) != ACB_OK) {
+            m->ra.alloc(n_tot * 8) != ACB_OK ||
+            (dpm && (m->hist1.alloc(n_tot * 4) != ACB_OK || m->hist2.alloc(n_tot * 4) != ACB_OK))) {
             set_last_error("DiT generate buffers allocation failed");
             return ACB_ERR_OOM;
         }
@@ -882,12 +893,13 @@ extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const f
     }
     ACB_TRY(m->condition(s));
 
-    // one graph per (shape, cfg, first, last): pack xt, evaluate, guidance, Euler / x0
-    auto get_graph = [&](int first, int last, cudaGraphExec_t * ex) -> acb_status {
+    // one graph per (shape, cfg, first, last, solver, history): pack xt, evaluate, guidance, then the
+    // solver step (Euler, or DPM++ 3M with min(step, 2) stored velocities) or the last step's x0
+    auto get_graph = [&](int first, int last, int hist, cudaGraphExec_t * ex) -> acb_status {
         uint32_t gbits = 0;  // the guidance scale is baked into the captured APG launch
         memcpy(&gbits, &guidance_scale, 4);
-        const auto key =
-            std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, first * 2 + last, m->exact ? 1 : 0, gbits);
+        const int  stepk = ((dpm ? 1 : 0) * 3 + hist) * 4 + first * 2 + last;
+        const auto key   = std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, stepk, m->exact ? 1 : 0, gbits);
         auto       it  = m->graphs.find(key);
         if (it != m->graphs.end()) {
             *ex = it->second;
@@ -907,7 +919,10 @@ extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const f
                              m->vt.as<float>(), (acb_stream_t) s);
             v  = m->vt.as<float>();
         }
-        if (st == ACB_OK) {
+        if (st == ACB_OK && dpm && !last) {
+            st = acb_dit_dpm3m(m->xt.as<float>(), v, m->hist1.as<float>(), m->hist2.as<float>(), hist,
+                               m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
+        } else if (st == ACB_OK) {
             st = acb_dit_euler(m->xt.as<float>(), v, m->tt.as<float>(), last, m->out.as<float>(), (int64_t) n_tot,
                                (acb_stream_t) s);
         }
@@ -935,7 +950,7 @@ extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const f
     for (int step = 0; step < num_steps && st == ACB_OK; step++) {
         const int       first = step == 0, last = step == num_steps - 1;
         cudaGraphExec_t ex    = nullptr;
-        st                    = get_graph(first, last, &ex);
+        st                    = get_graph(first, last, dpm ? (step < 2 ? step : 2) : 0, &ex);
         if (st != ACB_OK) {
             break;
         }

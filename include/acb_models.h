@@ -152,6 +152,15 @@ ACB_API int        acb_dit_eval_kernels(const acb_dit * m);
 ACB_API acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
                                     const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                     const float * schedule, float * output, float guidance_scale, float * gpu_ms);
+/* Solvers of acb_dit_generate_solver (the registry keys of solvers/solver-registry.h:30-32). */
+enum { ACB_SOLVER_EULER = 0, ACB_SOLVER_DPM3M = 1 };
+/* acb_dit_generate with dit_ggml_generate's solver choice (dit-sampler.h:391-398, 608-611): Euler or
+ * DPM++ 3M (acb_dit_dpm3m on the velocity after guidance, its history on the device; the last
+ * step is the x0 prediction for every solver). Other solver values: ACB_ERR_INVALID_ARG. */
+ACB_API acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, const float * context_latents,
+                                           const float * enc_hidden, int enc_S, int T, int N, int num_steps,
+                                           const float * schedule, float * output, float guidance_scale, int solver,
+                                           float * gpu_ms);
 ACB_API void       acb_dit_free(acb_dit * m);
 
 /* ---- Qwen3 causal LM (replaces src/qwen3-lm.h) ---------------------------------------------- */

@@ -551,12 +551,14 @@ def dit_from_gguf_tensors(cfg, tensors):
     return OracleDiT(oc_cfg, w)
 
 
-def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, momentum=-0.75, norm_threshold=2.5):
-    """dit_ggml_generate (src/dit-sampler.h:132-711) with the Euler solver over an OracleDiT:
-    batched CFG with APG in double when guidance_scale > 1 and a null condition is given.
-    Returns x0 [N][T][out_ch]."""
+def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, momentum=-0.75, norm_threshold=2.5,
+                 solver="euler"):
+    """dit_ggml_generate (src/dit-sampler.h:132-711) over an OracleDiT with the Euler solver or
+    DPM++ 3M (solver="dpm3m", solver-dpm.h:14-50): batched CFG with APG in double when
+    guidance_scale > 1 and a null condition is given. Returns x0 [N][T][out_ch]."""
     N, T, Oc = noise.shape
     xt = noise.astype(np.float32).copy()
+    hist1 = hist2 = None
     cfg_on = guidance_scale > 1.0 and null_emb is not None
     ra = None
     for step, t in enumerate(schedule):
@@ -582,6 +584,9 @@ def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, mo
             v = (cond + (guidance_scale - 1.0) * orth).astype(np.float32)
         if step == len(schedule) - 1:
             return (xt - v * np.float32(t)).astype(np.float32)
+        if solver == "dpm3m":
+            xt, hist1, hist2 = dpm3m_step(xt, v, hist1, hist2, t, schedule[step + 1])
+            continue
         dt = np.float32(np.float32(t) - np.float32(schedule[step + 1]))
         xt = (xt - v * dt).astype(np.float32)
     return xt

@@ -81,6 +81,10 @@ def test_dit_generate_cfg_apg_matches_oracle(cuda, tmp_path):
         ref = O.dit_generate(od, noise, ctx, enc, null, sched, g)
         assert np.isfinite(x0).all() and ms > 0
         _check(x0, ref, 0.9999, 1e-2, f"generate guidance {g}")
+    # DPM++ 3M through the same driver (Euler, second and third order steps, then the x0 step)
+    x0d, _ = dit.generate(noise, ctx, enc, sched, guidance_scale=3.0, solver="dpm3m")
+    _check(x0d, O.dit_generate(od, noise, ctx, enc, null, sched, 3.0, solver="dpm3m"), 0.9999, 1e-2,
+           "generate dpm3m")
     # repeat: the captured step graphs give identical results
     x0b, _ = dit.generate(noise, ctx, enc, sched, guidance_scale=3.0)
     x0c, _ = dit.generate(noise, ctx, enc, sched, guidance_scale=3.0)
