@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include "../../include/acb.h"
+#include "acb_exp.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #    error "libacb is built for sm_100a only"
@@ -104,9 +105,14 @@ __device__ __forceinline__ float warp_max(float v) {
 // ggml_rms_norm scale: sum of float squares accumulated in double, mean rounded to float,
 // 1/sqrt in IEEE float (the division and sqrt are correctly rounded under -prec-div/-prec-sqrt).
 // ggml_swiglu element: silu(g) * u with silu(g) = g / (1 + exp(-g)), IEEE division, each node
-// rounded once (every SwiGLU in the library uses this one definition).
+// rounded once, exp = acb_expf (every SwiGLU in the library uses this one definition, and the
+// same exp as any host program that includes acb_exp.h).
+__device__ __forceinline__ float silu_f(float g) {
+    return __fdiv_rn(g, __fadd_rn(1.0f, acb_expf(-g)));
+}
+
 __device__ __forceinline__ float silu_times(float g, float u) {
-    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    const float s = silu_f(g);
     return __fmul_rn(s, u);
 }
 

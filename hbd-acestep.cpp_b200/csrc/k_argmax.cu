@@ -38,7 +38,9 @@ __device__ Best block_best(Best s) {
     return r;
 }
 
-// scratch layout: float4 part[rows][nblk] (b1, b2, i1 bits, -) then int ticket[rows]
+// scratch layout: int ticket[ticket_rows] (padded to 256 bytes) at offset 0, then
+// float4 part[rows][nblk] (b1, b2, i1 bits, -). The tickets sit at the same offset for every
+// shape, so a buffer reused across (rows, V) never finds a stale partial where a counter lives.
 template <int PDL>
 __global__ void __launch_bounds__(256) argmax_kernel(const float * __restrict__ logits, int64_t stride, int64_t V,
                                                      int64_t chunk, int32_t * __restrict__ ids,
@@ -130,15 +132,19 @@ static int argmax_blocks(int64_t V) {
     return (int) (n < 1 ? 1 : (n > 128 ? 128 : n));
 }
 
+static size_t ticket_bytes(int ticket_rows) {
+    return ((size_t) ticket_rows * sizeof(int) + 255) / 256 * 256;
+}
+
 static acb_status launch_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
                                 float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
-                                int64_t hist_stride, const int32_t * hist_base, void * scratch, int flags,
-                                cudaStream_t stream) {
+                                int64_t hist_stride, const int32_t * hist_base, void * scratch, int ticket_rows,
+                                int flags, cudaStream_t stream) {
     const int nblk  = argmax_blocks(V);
     int64_t   chunk = (V + nblk - 1) / nblk;
     chunk           = (chunk + 3) / 4 * 4;
-    float4 *  part   = reinterpret_cast<float4 *>(scratch);
-    int *     ticket = reinterpret_cast<int *>(part + (size_t) rows * nblk);
+    int *     ticket = reinterpret_cast<int *>(scratch);
+    float4 *  part   = reinterpret_cast<float4 *>(reinterpret_cast<unsigned char *>(scratch) + ticket_bytes(ticket_rows));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim            = dim3((unsigned) nblk, (unsigned) rows);
     cfg.blockDim           = dim3(256);
@@ -168,22 +174,22 @@ extern "C" size_t acb_argmax_scratch_bytes(int rows, int64_t V) {
     if (rows <= 0 || V <= 0) {
         return 0;
     }
-    return (size_t) rows * argmax_blocks(V) * sizeof(float4) + (size_t) rows * sizeof(int) + 16;
+    return ticket_bytes(ACB_ARGMAX_MAX_ROWS) + (size_t) rows * argmax_blocks(V) * sizeof(float4);
 }
 
 extern "C" acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
                                  float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,
                                  int64_t hist_stride, const int32_t * hist_base, void * scratch, int flags,
                                  acb_stream_t stream) {
-    if (!logits || !ids || !scratch || V <= 0 || V > INT32_MAX || rows <= 0 || stride < V ||
-        (hist && (!pos_advance || !hist_base))) {
+    if (!logits || !ids || !scratch || V <= 0 || V > INT32_MAX || rows <= 0 || rows > ACB_ARGMAX_MAX_ROWS ||
+        stride < V || (hist && (!pos_advance || !hist_base))) {
         return ACB_ERR_INVALID_ARG;
     }
     if (reinterpret_cast<uintptr_t>(scratch) % 16 != 0) {
         return ACB_ERR_INVALID_ARG;
     }
     return launch_argmax(logits, stride, V, rows, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base,
-                         scratch, flags, (cudaStream_t) stream);
+                         scratch, ACB_ARGMAX_MAX_ROWS, flags, (cudaStream_t) stream);
 }
 
 // ---- variant with library-owned scratch (no allocation by the caller or the library) ------------
@@ -196,8 +202,8 @@ extern "C" acb_status acb_argmax(const float * logits, int64_t stride, int64_t V
 // exits.
 namespace acb {
 constexpr int    kNoallocRows  = ACB_ARGMAX_NOALLOC_MAX_ROWS;
-constexpr size_t kNoallocBytes = ((size_t) kNoallocRows * 128 * sizeof(float4) + kNoallocRows * sizeof(int) + 255) /
-                                 256 * 256;
+constexpr size_t kNoallocTicketBytes = ((size_t) kNoallocRows * sizeof(int) + 255) / 256 * 256;
+constexpr size_t kNoallocBytes       = kNoallocTicketBytes + (size_t) kNoallocRows * 128 * sizeof(float4);
 static __device__ __align__(256) unsigned char g_argmax_scratch[kNoallocBytes];
 
 // Device address of g_argmax_scratch per device ordinal. In host code the array's name is only a
@@ -207,22 +213,28 @@ static std::mutex g_scratch_mu;
 
 void set_last_error(const std::string & e);
 
-static acb_status noalloc_scratch(void ** out) {
+static acb_status noalloc_scratch(void ** out, cudaStream_t stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        set_last_error("acb_argmax_noalloc: no current CUDA device");
         return ACB_ERR_CUDA;
     }
     std::lock_guard<std::mutex> lk(g_scratch_mu);
     if (!g_scratch_addr[dev]) {
-        void *            p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
+        void *      p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_argmax_scratch);
         if (e != cudaSuccess || !p) {
             set_last_cuda_error(e);
             set_last_error("acb_argmax_noalloc: cudaGetSymbolAddress failed");
             return ACB_ERR_CUDA;
         }
-        // the ticket counters must start at zero; every call returns them to zero
-        if (cudaMemset(p, 0, kNoallocBytes) != cudaSuccess) {
+        // The array is zero when the module loads; clearing the ticket counters once more on the
+        // caller's stream orders the clear before this call's kernel whatever kind of stream
+        // (blocking, non-blocking, per-thread default) the caller uses.
+        e = cudaMemsetAsync(p, 0, kNoallocTicketBytes, stream);
+        if (e != cudaSuccess) {
+            set_last_cuda_error(e);
+            set_last_error("acb_argmax_noalloc: clearing the scratch counters failed");
             return ACB_ERR_CUDA;
         }
         g_scratch_addr[dev] = p;
@@ -240,16 +252,16 @@ extern "C" acb_status acb_argmax_noalloc(const float * logits, int64_t stride, i
         (hist && (!pos_advance || !hist_base))) {
         return ACB_ERR_INVALID_ARG;
     }
-    if (rows > kNoallocRows || acb_argmax_scratch_bytes(rows, V) > kNoallocBytes) {
+    if (rows > kNoallocRows) {
         set_last_error("acb_argmax_noalloc: rows exceeds ACB_ARGMAX_NOALLOC_MAX_ROWS (" +
                        std::to_string(kNoallocRows) + "); use acb_argmax with caller scratch");
         return ACB_ERR_UNSUPPORTED;
     }
     void *     scratch = nullptr;
-    acb_status st      = noalloc_scratch(&scratch);
+    acb_status st      = noalloc_scratch(&scratch, (cudaStream_t) stream);
     if (st != ACB_OK) {
         return st;
     }
     return launch_argmax(logits, stride, V, rows, ids, margin, pos_advance, hist, mhist, hist_stride, hist_base,
-                         scratch, flags, (cudaStream_t) stream);
+                         scratch, kNoallocRows, flags, (cudaStream_t) stream);
 }

@@ -3,14 +3,15 @@
 // over the cache, and the greedy argmax that feeds the next step's embedding gather.
 //
 // Attention reproduces ggml-CPU's qwen3_attn_f32 on an f16 cache (src/qwen3-enc.h:101-112):
-//   s_j = (f16(q) . k_j) * scale                 f32 accumulation
-//   p_j = f16( expf(s_j - max) * (float)(1/sum) ) sum of expf in double
-//   o   = sum_j p_j v_j                           f32 accumulation
-// The normalised probabilities are rounded before the PV product, so the step runs in two
-// passes over split chunks of the cache: pass 1 writes scores and per-split maxima, pass 2
-// normalises and forms per-split partial outputs, and the last split CTA of each head sums the
-// partials in split order. Every CTA of a head computes the same global sum in the same order,
-// so all splits use identical normalisers.
+//   s_j = (float)(f16(q) . k_j) * scale                  double accumulation of exact products
+//   p_j = f16( exp(s_j - max) * (float)(1/sum) )         sum of exp in double, exp = acb_expf
+//   o   = (float) sum_j p_j v_j                          double accumulation of exact products
+// Products of two f16 values are exact in float, and their double sum is exact unless the
+// terms span ~24 binades, so every split count and lane order gives the same floats (and the
+// oracle's serial loops give them too). The normalised probabilities are rounded before the PV
+// product, so the step runs in two passes over split chunks of the cache: pass 1 writes scores
+// and per-split maxima, pass 2 normalises and forms per-split partial outputs (double), and
+// the last split CTA of each head adds the partials and rounds once.
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -190,15 +191,15 @@ __global__ void __launch_bounds__(128) attn_scores_kernel(const float * __restri
             }
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                float acc = 0.0f;
+                double acc = 0.0;
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    acc = __fadd_rn(acc, __fmul_rn(kf[e], qv[g][e]));
+                    acc += (double) __fmul_rn(kf[e], qv[g][e]);
                 }
                 acc += __shfl_xor_sync(0xffffffffu, acc, 1);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 2);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-                const float sv = __fmul_rn(acc, scale);
+                const float sv = __fmul_rn((float) acc, scale);
                 if (j < j1) {
                     if (sub == 0) {
                         scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j] = sv;
@@ -231,7 +232,7 @@ template <int G, int PDL>
 __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__ scores, int64_t s_stride,
                                                       const float * __restrict__ smax, int Nh, int Nkv,
                                                       const int32_t * __restrict__ pos, KvLayout kv, int n_split,
-                                                      float * __restrict__ part, float * __restrict__ out,
+                                                      double * __restrict__ part, float * __restrict__ out,
                                                       int64_t out_stride, int * __restrict__ tickets) {
     constexpr int D = 128;
     dep_wait<PDL>();
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
         const float * sr = scores + (int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride;
         double        s  = 0.0;
         for (int j = threadIdx.x; j < kv_len; j += 128) {
-            s += (double) expf(__fsub_rn(sr[j], M[g]));
+            s += (double) acb_expf(__fsub_rn(sr[j], M[g]));
         }
         s = warp_sum(s);
         if (lane == 0) {
@@ -282,12 +283,12 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
     __syncthreads();
 
     // partial output over this chunk: lane owns 4 of the D elements, warps split the keys
-    float acc[G][4];
+    double acc[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++) {
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-            acc[g][e] = 0.0f;
+            acc[g][e] = 0.0;
         }
     }
     const uint16_t * vb = kv.v + kv_index(kv, Nkv, D, set, hk, 0);
@@ -315,39 +316,38 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
                 const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].y));
 #pragma unroll
                 for (int g = 0; g < G; g++) {
-                    const float pe = __fmul_rn(expf(__fsub_rn(sv[u][g], sM[g])), sInv[g]);
+                    const float pe = __fmul_rn(acb_expf(__fsub_rn(sv[u][g], sM[g])), sInv[g]);
                     const float pp = __half2float(__float2half_rn(pe));
-                    acc[g][0]      = __fadd_rn(acc[g][0], __fmul_rn(f01.x, pp));
-                    acc[g][1]      = __fadd_rn(acc[g][1], __fmul_rn(f01.y, pp));
-                    acc[g][2]      = __fadd_rn(acc[g][2], __fmul_rn(f23.x, pp));
-                    acc[g][3]      = __fadd_rn(acc[g][3], __fmul_rn(f23.y, pp));
+                    acc[g][0] += (double) __fmul_rn(f01.x, pp);
+                    acc[g][1] += (double) __fmul_rn(f01.y, pp);
+                    acc[g][2] += (double) __fmul_rn(f23.x, pp);
+                    acc[g][3] += (double) __fmul_rn(f23.y, pp);
                 }
             }
         }
     }
     // reduce the 4 warps through shared memory, then write the split partial [t][split][Nh*D]
-    __shared__ float4 wacc[4][G][32];
+    __shared__ double4 wacc[4][G][32];
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        wacc[warp][g][lane] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+        wacc[warp][g][lane] = make_double4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
     }
     __syncthreads();
-    if (warp < G) {
-        const int g = warp;
-        float4    r = wacc[0][g][lane];
+    for (int g = warp; g < G; g += 4) {
+        double4 r = wacc[0][g][lane];
 #pragma unroll
         for (int w = 1; w < 4; w++) {
-            const float4 o = wacc[w][g][lane];
-            r.x            = __fadd_rn(r.x, o.x);
-            r.y            = __fadd_rn(r.y, o.y);
-            r.z            = __fadd_rn(r.z, o.z);
-            r.w            = __fadd_rn(r.w, o.w);
+            const double4 o = wacc[w][g][lane];
+            r.x += o.x;
+            r.y += o.y;
+            r.z += o.z;
+            r.w += o.w;
         }
-        float4 * dst = reinterpret_cast<float4 *>(part + ((int64_t) t * n_split + split) * Nh * D +
-                                                  (int64_t) (hk * G + g) * D + lane * 4);
-        *dst         = r;
-        __threadfence();
+        double * dst = part + ((int64_t) t * n_split + split) * Nh * D + (int64_t) (hk * G + g) * D + lane * 4;
+        reinterpret_cast<double2 *>(dst)[0] = make_double2(r.x, r.y);
+        reinterpret_cast<double2 *>(dst)[1] = make_double2(r.z, r.w);
     }
+    __threadfence();
     if (!out) {
         return;
     }
@@ -363,19 +363,16 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
         return;
     }
     __threadfence();
-    for (int idx = threadIdx.x; idx < G * 32; idx += blockDim.x) {
-        const int     g   = idx >> 5, l = idx & 31;
-        const int64_t off = (int64_t) (hk * G + g) * D + l * 4;
-        float4        a   = __ldcg(reinterpret_cast<const float4 *>(part + (int64_t) t * n_split * Nh * D + off));
-        for (int s = 1; s < n_split; s++) {
-            const float4 b =
-                __ldcg(reinterpret_cast<const float4 *>(part + ((int64_t) t * n_split + s) * Nh * D + off));
-            a.x = __fadd_rn(a.x, b.x);
-            a.y = __fadd_rn(a.y, b.y);
-            a.z = __fadd_rn(a.z, b.z);
-            a.w = __fadd_rn(a.w, b.w);
+    for (int idx = threadIdx.x; idx < G * 64; idx += blockDim.x) {
+        const int     g   = idx >> 6, l = idx & 63;
+        const int64_t off = (int64_t) (hk * G + g) * D + l * 2;
+        double2       a   = make_double2(0.0, 0.0);
+        for (int s = 0; s < n_split; s++) {
+            const double2 b = __ldcg(reinterpret_cast<const double2 *>(part + ((int64_t) t * n_split + s) * Nh * D + off));
+            a.x += b.x;
+            a.y += b.y;
         }
-        *reinterpret_cast<float4 *>(out + (int64_t) t * out_stride + off) = a;
+        *reinterpret_cast<float2 *>(out + (int64_t) t * out_stride + off) = make_float2((float) a.x, (float) a.y);
     }
     if (threadIdx.x == 0) {
         tickets[t * Nkv + hk] = 0;
@@ -442,7 +439,7 @@ extern "C" int acb_attn_decode_splits(int n_tok, int Nkv) {
 extern "C" acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok, int Nh, int Nkv, int head_dim,
                                       const int32_t * pos, const uint16_t * k_cache, const uint16_t * v_cache,
                                       int max_seq, int set0, int set_per_tok, float scale, int n_split,
-                                      float * scores, float * smax, float * part, float * out, int64_t out_stride,
+                                      float * scores, float * smax, double * part, float * out, int64_t out_stride,
                                       int * tickets, int flags, acb_stream_t stream) {
     if (!q || !pos || !k_cache || !v_cache || !scores || !smax || !part || n_tok <= 0 || Nh <= 0 || Nkv <= 0 ||
         n_split < 1 || max_seq <= 0 || (out && !tickets)) {

@@ -32,8 +32,10 @@
 // Arithmetic per op is that of the per-op kernels: activation quantisation of quantize_q8_0,
 // exact integer dot products per Q8_0 block scaled by d_w * d_x (dp4a here, the int8 MMA of
 // gemv_tiles_kernel there), q/k-norm + RoPE of qkv_post_kernel, the two-pass f16-cache softmax
-// of attn_scores_kernel / attn_pv_kernel, the argmax of argmax_kernel. Only the partition (8
-// consumer warps, 4 lanes per row, split count, tile ranges) decides the order of the float sums.
+// of attn_scores_kernel / attn_pv_kernel, the argmax of argmax_kernel. Every sum whose order
+// the partition decides (8 consumer warps, 4 lanes per row, split count, tile ranges) is formed
+// in double from float terms and rounded to float once, so this kernel, the per-op graph and
+// the CPU oracle produce the same floats and the same greedy tokens.
 #include <cstdlib>
 #include <string>
 
@@ -65,16 +67,17 @@ constexpr uint64_t kBarrierNs     = 2000000000ull;  // grid barrier time limit
 constexpr int kSmFull   = 0;     // uint64 full[16]
 constexpr int kSmEmpty  = 128;   // uint64 empty[16]
 constexpr int kSmRed    = 256;   // double [16][4]
-constexpr int kSmMisc   = 768;   // float inv[4], int flags
-constexpr int kSmGate   = 2048;  // float [256] gate rows of this CTA's SwiGLU tiles; residual rows
-constexpr int kSmAct    = 3072;  // int8 xq[kPdMaxK] + float xd[kPdMaxK/32]; attention scratch
-constexpr int kSmTredG  = kSmAct + kPdMaxK + kPdMaxK / 32 * 4;  // float [8 tiles][8 warps][16 rows]
-constexpr int kSmRing   = (kSmTredG + kPdWarps * kPdWarps * 16 * 4 + 127) / 128 * 128;
+constexpr int kSmMisc   = 768;   // float inv[4], float max[4], int flags (up to byte 808)
+constexpr int kSmGate   = 1024;  // float [256] gate rows of this CTA's SwiGLU tiles; residual rows
+constexpr int kSmAct    = 2048;  // int8 xq[kPdMaxK] + f16 xd[kPdMaxK/32]; attention scratch
+constexpr int kSmTredG  = kSmAct + kPdMaxK + kPdMaxK / 32 * 2;  // double [8 tiles][8 warps][16 rows]
+constexpr int kSmRing   = (kSmTredG + kPdWarps * kPdWarps * 16 * 8 + 127) / 128 * 128;
 // attention scratch inside the activation region
 constexpr int kAtQ      = 0;      // float [G][128] f16-rounded q
 constexpr int kAtKp     = 2048;   // float [128] the new k (f16-rounded)
-constexpr int kAtAcc    = 2560;   // float4 [8 warps][32] (P.V partials; the combine uses 256)
+constexpr int kAtAcc    = 2560;   // double4 [8 warps][32] (P.V partials; the combine uses 256)
 constexpr int kAtMax    = 10752;  // float [16][G]
+static_assert(kAtMax + 16 * 4 * 4 <= kPdMaxK + kPdMaxK / 32 * 2, "attention scratch fits the activation region");
 
 extern __shared__ __align__(128) uint8_t pd_smem[];
 
@@ -82,14 +85,15 @@ extern __shared__ __align__(128) uint8_t pd_smem[];
 __device__ __forceinline__ uint64_t * sm_full() { return reinterpret_cast<uint64_t *>(pd_smem + kSmFull); }
 __device__ __forceinline__ uint64_t * sm_empty() { return reinterpret_cast<uint64_t *>(pd_smem + kSmEmpty); }
 __device__ __forceinline__ double * sm_red() { return reinterpret_cast<double *>(pd_smem + kSmRed); }
+__device__ __forceinline__ double * sm_tredd() { return reinterpret_cast<double *>(pd_smem + kSmTredG); }
 __device__ __forceinline__ float * sm_misc() { return reinterpret_cast<float *>(pd_smem + kSmMisc); }
 __device__ __forceinline__ volatile int * sm_abort() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 32); }
 __device__ __forceinline__ volatile int * sm_last() { return reinterpret_cast<volatile int *>(pd_smem + kSmMisc + 36); }
-__device__ __forceinline__ float * sm_tredg() { return reinterpret_cast<float *>(pd_smem + kSmTredG); }
 __device__ __forceinline__ uint8_t * sm_act() { return pd_smem + kSmAct; }
 __device__ __forceinline__ float * sm_gate() { return reinterpret_cast<float *>(pd_smem + kSmGate); }
 __device__ __forceinline__ int8_t * sm_xq() { return reinterpret_cast<int8_t *>(pd_smem + kSmAct); }
-__device__ __forceinline__ float * sm_xd() { return reinterpret_cast<float *>(pd_smem + kSmAct + kPdMaxK); }
+// activation block scales: f16 values (the scale is rounded to f16 by the quantiser), stored as f16
+__device__ __forceinline__ __half * sm_xd() { return reinterpret_cast<__half *>(pd_smem + kSmAct + kPdMaxK); }
 __device__ __forceinline__ uint8_t * sm_ring() { return pd_smem + kSmRing; }
 
 struct PdParams {
@@ -101,7 +105,7 @@ struct PdParams {
     float *         qkv;
     float *         scores;  // [Nh][max_seq]
     float *         smax;    // [Nh][kPdMaxSplit]
-    float *         part;    // [kPdMaxSplit][Nh][D]
+    double *        part;    // [kPdMaxSplit][Nh][D]
     float *         att;     // [Nh*D]
     float *         gu;      // [F] silu(gate) * up
     float4 *        bpart;   // [n_ctas]
@@ -128,7 +132,7 @@ ScratchMap scratch_map(const acb_decode_step & s, int n_ctas) {
     m.smax   = o;
     o        = al(o + 4 * (size_t) s.n_heads * kPdMaxSplit);
     m.part   = o;
-    o        = al(o + 4 * (size_t) kPdMaxSplit * qd);
+    o        = al(o + 8 * (size_t) kPdMaxSplit * qd);
     m.att    = o;
     o        = al(o + 4 * qd);
     m.gu     = o;
@@ -459,7 +463,7 @@ __device__ void pd_act_quant_n(const PdParams & P, PdCtx & x, const float * src,
                 (uint32_t) (q0 & 0xff) | ((uint32_t) (q1 & 0xff) << 8) | ((uint32_t) (q2 & 0xff) << 16) |
                 ((uint32_t) (q3 & 0xff) << 24);
             if ((f & 7) == 0) {
-                sm_xd()[f >> 3] = __half2float(__float2half_rn(d));
+                sm_xd()[f >> 3] = __float2half_rn(d);
             }
         }
     }
@@ -490,16 +494,23 @@ enum { EPI_STORE = 0, EPI_ADD = 1, EPI_HEAD = 2, EPI_GATE = 3, EPI_UP = 4 };
 
 // One 16-row x 32-column tile block for one activation column. Lane 4g + q holds bytes
 // 4q..4q+3 and 16+4q..16+4q+3 of rows g and g + 8 (the tile order) and the activation words q
-// and 4 + q (xw); two dp4a per row give its integer partial sum over those 8 columns, scaled by
-// d_w * d_x of the block into the lane's float partials of the two rows.
-__device__ __forceinline__ void pd_block(const uint4 & a, uint32_t dw, uint2 xw, float dx, float & acc0,
-                                         float & acc2) {
-    const int   s0 = __dp4a((int) a.z, (int) xw.y, __dp4a((int) a.x, (int) xw.x, 0));
-    const int   s1 = __dp4a((int) a.w, (int) xw.y, __dp4a((int) a.y, (int) xw.x, 0));
+// and 4 + q (xw); two dp4a per row give its integer partial sum over those 8 columns. The four
+// lanes of a row add their integer sums exactly (shuffles), and one lane turns the block's sum
+// into its float term (float)isum * (d_w * d_x), added in double to the lane's partials.
+__device__ __forceinline__ void pd_block(const uint4 & a, uint32_t dw, uint2 xw, float dx, double & acc0,
+                                         double & acc2, bool lead) {
+    int s0 = __dp4a((int) a.z, (int) xw.y, __dp4a((int) a.x, (int) xw.x, 0));
+    int s1 = __dp4a((int) a.w, (int) xw.y, __dp4a((int) a.y, (int) xw.x, 0));
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
+    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
     const float dl = f16_bits_to_f((uint16_t) (dw & 0xffff));
     const float dh = f16_bits_to_f((uint16_t) (dw >> 16));
-    acc0           = __fmaf_rn((float) s0, __fmul_rn(dl, dx), acc0);
-    acc2           = __fmaf_rn((float) s1, __fmul_rn(dh, dx), acc2);
+    if (lead) {
+        acc0 += (double) __fmul_rn((float) s0, __fmul_rn(dl, dx));
+        acc2 += (double) __fmul_rn((float) s1, __fmul_rn(dh, dx));
+    }
 }
 
 // Q8_0 tile GEMV over this CTA's tile range for one activation column: warp w takes 8
@@ -532,7 +543,7 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
     for (int64_t tg = t0; tg < t1; tg += kPdWarps) {
         const int nt = (int) min((int64_t) kPdWarps, t1 - tg);
         for (int j = 0; j < nt; j++) {
-        float acc0 = 0.0f, acc2 = 0.0f;  // rows g and g + 8, this lane's 8 of every 32 columns
+        double acc0 = 0.0, acc2 = 0.0;  // rows g and g + 8: block terms (added by lane q == 0)
         for (int b0 = 0; b0 < nb; b0 += bs) {
             const int       s    = (int) (x.it % (uint32_t) P.slots);
             const bool      have = pd_wait_full(P, x, s, (x.it / (uint32_t) P.slots) & 1);
@@ -540,12 +551,12 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
             // warp w takes nbw consecutive blocks of the stage; every shared-memory operand of
             // its blocks is loaded first. Lane 4g + q holds bytes 4q..4q+3 and 16+4q..16+4q+3 of
             // rows g and g + 8 (the tile order); its two dp4a pairs give those rows' partial sums
-            // over its 8 columns, scaled per block (d_w * d_x) into per-lane float partials
-            // that are added over the 4 lanes of a row at the end of the tile.
+            // over its 8 columns, the 4 lanes of a row add them exactly, and lane q == 0 adds the
+            // block's float term to its double partials.
             const int nbw = (bs + kPdWarps - 1) / kPdWarps, bw0 = warp * nbw;
             if (nbw == kPdBpw && bw0 + kPdBpw <= bs && (b0 & 3) == 0) {
-                // all of this warp's blocks are in the stage: constant offsets (the scales of
-                // blocks bb.. are read as 16-byte aligned float4: bb is a multiple of 4)
+                // all of this warp's blocks are in the stage: constant offsets (the f16 scales of
+                // blocks bb.. are read as 8-byte aligned quads: bb is a multiple of 4)
                 const uint8_t * sp = st + bw0 * kPdTileBlk;
                 const int       bb = b0 + bw0;
                 uint4           a[kPdBpw];
@@ -560,17 +571,18 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
                 float dx[kPdBpw];
 #pragma unroll
                 for (int u = 0; u < kPdBpw; u += 4) {
-                    const float4 d4 = *reinterpret_cast<const float4 *>(sm_xd() + bb + u);
-                    dx[u]           = d4.x;
-                    dx[u + 1]       = d4.y;
-                    dx[u + 2]       = d4.z;
-                    dx[u + 3]       = d4.w;
+                    const uint2   d4 = *reinterpret_cast<const uint2 *>(sm_xd() + bb + u);
+                    const float2  lo = __half22float2(*reinterpret_cast<const __half2 *>(&d4.x));
+                    const float2  hi = __half22float2(*reinterpret_cast<const __half2 *>(&d4.y));
+                    dx[u]           = lo.x;
+                    dx[u + 1]       = lo.y;
+                    dx[u + 2]       = hi.x;
+                    dx[u + 3]       = hi.y;
                 }
-                if (have) {
+                // the shuffles inside run on every lane; the terms are added only with the stage
 #pragma unroll
-                    for (int u = 0; u < kPdBpw; u++) {
-                        pd_block(a[u], dw[u], xw[u], dx[u], acc0, acc2);
-                    }
+                for (int u = 0; u < kPdBpw; u++) {
+                    pd_block(a[u], dw[u], xw[u], dx[u], acc0, acc2, have && q == 0);
                 }
             } else {
                 // ragged stage: indices past it are clamped to its last block (loads stay
@@ -582,10 +594,8 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
                     const uint4 a  = *reinterpret_cast<const uint4 *>(st + bl * kPdTileBlk + lane * 16);
                     const uint32_t dw = *reinterpret_cast<const uint32_t *>(st + bl * kPdTileBlk + 512 + g * 4);
                     const uint2 xw = *reinterpret_cast<const uint2 *>(xq4 + 8 * b + 2 * q);
-                    const float dx = sm_xd()[b];
-                    if (have && u < nbw && bw0 + u < bs) {
-                        pd_block(a, dw, xw, dx, acc0, acc2);
-                    }
+                    const float dx = __half2float(sm_xd()[b]);
+                    pd_block(a, dw, xw, dx, acc0, acc2, have && q == 0 && u < nbw && bw0 + u < bs);
                 }
             }
             __syncwarp();
@@ -594,25 +604,22 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
             }
             x.it++;
         }
-        acc0 = __fadd_rn(acc0, __shfl_xor_sync(0xffffffffu, acc0, 1));
-        acc2 = __fadd_rn(acc2, __shfl_xor_sync(0xffffffffu, acc2, 1));
-        acc0 = __fadd_rn(acc0, __shfl_xor_sync(0xffffffffu, acc0, 2));
-        acc2 = __fadd_rn(acc2, __shfl_xor_sync(0xffffffffu, acc2, 2));
         if (q == 0) {
-            float * tr = sm_tredg() + (j * kPdWarps + warp) * 16;
-            tr[g]      = acc0;
-            tr[g + 8]  = acc2;
+            double * tr = sm_tredd() + (j * kPdWarps + warp) * 16;
+            tr[g]       = acc0;
+            tr[g + 8]   = acc2;
         }
         }
         cons_sync();
         if (warp < nt && lane < 16) {
             const int64_t t  = tg + warp;
-            const float * tr = sm_tredg() + warp * kPdWarps * 16;
-            float         v  = 0.0f;
+            const double * tr = sm_tredd() + warp * kPdWarps * 16;
+            double         vd = 0.0;
 #pragma unroll
             for (int w = 0; w < kPdWarps; w++) {
-                v = __fadd_rn(v, tr[w * 16 + lane]);
+                vd += tr[w * 16 + lane];
             }
+            const float v = (float) vd;
             const int64_t row = t * 16 + lane;
             if (EPI == EPI_ADD) {
                 y[row] = __fadd_rn(t - t0 < kPdWarps ? resv : __ldcg(y + row), v);
@@ -808,15 +815,15 @@ __device__ void pd_attn_scores(const PdParams & P, PdCtx & x, const acb_decode_l
             }
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                float acc = 0.0f;
+                double acc = 0.0;  // products of f16 values are exact in float
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    acc = __fadd_rn(acc, __fmul_rn(kf[e], qv[g][e]));
+                    acc += (double) __fmul_rn(kf[e], qv[g][e]);
                 }
                 acc += __shfl_xor_sync(0xffffffffu, acc, 1);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 2);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-                const float sv = __fmul_rn(acc, S.attn_scale);
+                const float sv = __fmul_rn((float) acc, S.attn_scale);
                 if (j < j1) {
                     if (sub == 0) {
                         P.scores[(int64_t) (h * G + g) * S.max_seq + j] = sv;
@@ -924,7 +931,7 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
 #pragma unroll
             for (int u = 0; u < US; u++) {
                 if (j + u * kPdCons < kv_len) {
-                    s += (double) expf(__fsub_rn(t[u], M[gg]));
+                    s += (double) acb_expf(__fsub_rn(t[u], M[gg]));
                 }
             }
         }
@@ -943,19 +950,19 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
     }
     cons_sync();
     const float Mg = M[g], ig = sm_misc()[g];
-    float4      acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    double4     acc = make_double4(0.0, 0.0, 0.0, 0.0);
     for (;;) {
 #pragma unroll
         for (int u = 0; u < UV; u++) {
             const int j = jb + WPH * u;
             if (j < j1) {
-                const float  pp  = f16r(__fmul_rn(expf(__fsub_rn(sv[u], Mg)), ig));
+                const float  pp  = f16r(__fmul_rn(acb_expf(__fsub_rn(sv[u], Mg)), ig));
                 const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[u].x));
                 const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[u].y));
-                acc.x            = __fadd_rn(acc.x, __fmul_rn(f01.x, pp));
-                acc.y            = __fadd_rn(acc.y, __fmul_rn(f01.y, pp));
-                acc.z            = __fadd_rn(acc.z, __fmul_rn(f23.x, pp));
-                acc.w            = __fadd_rn(acc.w, __fmul_rn(f23.y, pp));
+                acc.x += (double) __fmul_rn(f01.x, pp);
+                acc.y += (double) __fmul_rn(f01.y, pp);
+                acc.z += (double) __fmul_rn(f23.x, pp);
+                acc.w += (double) __fmul_rn(f23.y, pp);
             }
         }
         jb += WPH * UV;
@@ -964,19 +971,21 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
         }
         load_pv(jb);
     }
-    float4 * wacc = reinterpret_cast<float4 *>(sm_act() + kAtAcc);
+    double4 * wacc = reinterpret_cast<double4 *>(sm_act() + kAtAcc);
     wacc[warp * 32 + lane] = acc;
     cons_sync();
     if (wi == 0) {
-        float4 r = wacc[warp * 32 + lane];
+        double4 r = wacc[warp * 32 + lane];
         for (int w = 1; w < WPH; w++) {
-            const float4 o = wacc[(warp + w) * 32 + lane];
-            r.x            = __fadd_rn(r.x, o.x);
-            r.y            = __fadd_rn(r.y, o.y);
-            r.z            = __fadd_rn(r.z, o.z);
-            r.w            = __fadd_rn(r.w, o.w);
+            const double4 o = wacc[(warp + w) * 32 + lane];
+            r.x += o.x;
+            r.y += o.y;
+            r.z += o.z;
+            r.w += o.w;
         }
-        __stcg(reinterpret_cast<float4 *>(P.part + ((int64_t) sp * Nh + hq) * kPdD) + lane, r);
+        double2 * dst = reinterpret_cast<double2 *>(P.part + ((int64_t) sp * Nh + hq) * kPdD + lane * 4);
+        __stcg(dst, make_double2(r.x, r.y));
+        __stcg(dst + 1, make_double2(r.z, r.w));
         __threadfence();
     }
     cons_sync();
@@ -989,47 +998,46 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
         return;
     }
     // last split CTA of the head: thread (q, g, l) adds splits [q ns / Q, (q + 1) ns / Q) in
-    // order, then the Q partial sums are added in order
+    // double, then the Q partial sums are added in double and rounded to float once
     __threadfence();
-    constexpr int Q    = kPdWarps / G;  // split ranges (G * 32 * Q == 512)
+    constexpr int Q    = kPdWarps / G;  // split ranges (G * 32 * Q == 256)
     constexpr int QMAX = (kPdMaxSplit + Q - 1) / Q;
     const int     q    = tid / (G * 32), gl = tid % (G * 32);
     const int     s0   = q * ns / Q, s1 = (q + 1) * ns / Q;
     const int64_t off  = (int64_t) (h * G) * kPdD + gl * 4;
-    float4        v[QMAX];
+    double4       a    = make_double4(0.0, 0.0, 0.0, 0.0);
 #pragma unroll
-    for (int i = 0; i < QMAX; i++) {
-        const int si = min(s0 + i, ns - 1);  // clamped: added only if in the range
-        v[i]         = __ldcg(reinterpret_cast<const float4 *>(P.part + (int64_t) si * Nh * kPdD + off));
-    }
-    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int i0 = 0; i0 < QMAX; i0 += 4) {
+        double2 v[4][2];
 #pragma unroll
-    for (int i = 0; i < QMAX; i++) {
-        if (s0 + i < s1) {
-            a = i == 0 ? v[0] : make_float4(__fadd_rn(a.x, v[i].x), __fadd_rn(a.y, v[i].y), __fadd_rn(a.z, v[i].z),
-                                            __fadd_rn(a.w, v[i].w));
+        for (int i = 0; i < 4; i++) {
+            const int       si = min(s0 + i0 + i, ns - 1);  // clamped: added only if in the range
+            const double2 * src = reinterpret_cast<const double2 *>(P.part + (int64_t) si * Nh * kPdD + off);
+            v[i][0]             = __ldcg(src);
+            v[i][1]             = __ldcg(src + 1);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            if (i0 + i < QMAX && s0 + i0 + i < s1) {
+                a.x += v[i][0].x;
+                a.y += v[i][0].y;
+                a.z += v[i][1].x;
+                a.w += v[i][1].y;
+            }
         }
     }
     wacc[tid] = a;  // the block reduction above is complete (cons_sync after the ticket)
     cons_sync();
     if (tid < G * 32) {
-        float4 r  = wacc[tid];
-        bool   hv = 0 < (ns / Q);  // range 0 non-empty
+        double4 r = wacc[tid];
         for (int qq = 1; qq < Q; qq++) {
-            if ((qq + 1) * ns / Q > qq * ns / Q) {
-                const float4 o = wacc[qq * G * 32 + tid];
-                if (!hv) {
-                    r  = o;
-                    hv = true;
-                } else {
-                    r.x = __fadd_rn(r.x, o.x);
-                    r.y = __fadd_rn(r.y, o.y);
-                    r.z = __fadd_rn(r.z, o.z);
-                    r.w = __fadd_rn(r.w, o.w);
-                }
-            }
+            const double4 o = wacc[qq * G * 32 + tid];
+            r.x += o.x;
+            r.y += o.y;
+            r.z += o.z;
+            r.w += o.w;
         }
-        __stcg(reinterpret_cast<float4 *>(P.att + off), r);
+        __stcg(reinterpret_cast<float4 *>(P.att + off), make_float4((float) r.x, (float) r.y, (float) r.z, (float) r.w));
         if (tid == 0) {
             P.tickets[h] = 0;
         }
@@ -1326,7 +1334,7 @@ extern "C" acb_status acb_lm_decode_step(const acb_decode_step * step, acb_strea
     P.qkv     = reinterpret_cast<float *>(sc + m.qkv);
     P.scores  = reinterpret_cast<float *>(sc + m.scores);
     P.smax    = reinterpret_cast<float *>(sc + m.smax);
-    P.part    = reinterpret_cast<float *>(sc + m.part);
+    P.part    = reinterpret_cast<double *>(sc + m.part);
     P.att     = reinterpret_cast<float *>(sc + m.att);
     P.gu      = reinterpret_cast<float *>(sc + m.gu);
     P.bpart   = reinterpret_cast<float4 *>(sc + m.bpart);

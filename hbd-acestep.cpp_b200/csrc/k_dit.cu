@@ -30,7 +30,7 @@ __global__ void silu_kernel(const float * __restrict__ x, float * __restrict__ y
     const int64_t i = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) {
         const float v = x[i];
-        y[i]          = __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+        y[i]          = silu_f(v);
     }
 }
 

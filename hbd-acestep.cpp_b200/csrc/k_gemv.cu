@@ -9,6 +9,10 @@
 //   - the activation is quantised inside the kernel exactly like ggml-CPU's quantised mul_mat
 //     (Q8_0 blocks for Q8_0 weights, Q8_K for K-quants), and the dot products are integer
 //     dp4a sums scaled per block, so each block's contribution equals the CPU's;
+//   - a row's block terms are added in double and rounded to float once: the double sum of
+//     float terms is exact unless they span ~20 binades, so the float result does not depend
+//     on how lanes, warps and CTAs split the row (the oracle and the persistent decode step
+//     give the same bits);
 //   - fused prologues build the activation from its producer's output (RMSNorm*w, the sum of
 //     attention split partials, or SwiGLU of a gate|up row); the epilogue optionally adds a
 //     residual (ggml_add(hidden, out));
@@ -60,11 +64,13 @@ template <int PRO> __device__ __forceinline__ ActRaw<PRO> act_load(const GemvPar
     ActRaw<PRO>   r{ 0.0f, 0.0f };
     const float * row = p.x + (int64_t) m * p.x_stride;
     if (PRO == PRO_SUM_SPLITS) {
-        float s = row[k];
-        for (int i = 1; i < p.n_split; i++) {
-            s = __fadd_rn(s, row[(int64_t) i * p.K + k]);
+        // partials in double (the attention's split partials): summed, then rounded once
+        const double * rd = reinterpret_cast<const double *>(p.x) + (int64_t) m * p.x_stride;
+        double         s  = 0.0;
+        for (int i = 0; i < p.n_split; i++) {
+            s += rd[(int64_t) i * p.K + k];
         }
-        r.a = s;
+        r.a = (float) s;
     } else if (PRO == PRO_SWIGLU) {
         r.a = row[k];
         r.b = row[p.K + k];
@@ -83,7 +89,7 @@ template <int PRO> __device__ __forceinline__ float act_finish(const GemvParams 
         return p.norm_w ? __fmul_rn(v, r.b) : v;
     }
     if (PRO == PRO_SWIGLU) {
-        return __fmul_rn(__fdiv_rn(r.a, __fadd_rn(1.0f, expf(-r.a))), r.b);
+        return silu_times(r.a, r.b);
     }
     return r.a;
 }
@@ -125,27 +131,32 @@ __device__ float rms_scale_block(const GemvParams & p, int m, double * red) {
 template <int PRO>
 __device__ __forceinline__ void act_block32(const GemvParams & p, int m, int k0, float sc, bool vec, float * v) {
     const float * row = p.x + (int64_t) m * p.x_stride;
+    if (PRO == PRO_SUM_SPLITS) {
+        const double * rd = reinterpret_cast<const double *>(p.x) + (int64_t) m * p.x_stride + k0;
+        double         a[32];
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+            a[e] = 0.0;
+        }
+        for (int s = 0; s < p.n_split; s++) {
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                a[e] += rd[(int64_t) s * p.K + e];
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e++) {
+            v[e] = (float) a[e];
+        }
+        return;
+    }
     if (vec) {
         float4 a[8], b[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             a[i] = *reinterpret_cast<const float4 *>(row + k0 + 4 * i);
         }
-        if (PRO == PRO_SUM_SPLITS) {
-            for (int s = 1; s < p.n_split; s++) {
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    b[i] = *reinterpret_cast<const float4 *>(row + (int64_t) s * p.K + k0 + 4 * i);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    a[i].x = __fadd_rn(a[i].x, b[i].x);
-                    a[i].y = __fadd_rn(a[i].y, b[i].y);
-                    a[i].z = __fadd_rn(a[i].z, b[i].z);
-                    a[i].w = __fadd_rn(a[i].w, b[i].w);
-                }
-            }
-        } else if (PRO == PRO_SWIGLU) {
+        if (PRO == PRO_SWIGLU) {
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 b[i] = *reinterpret_cast<const float4 *>(row + p.K + k0 + 4 * i);
@@ -300,7 +311,7 @@ __device__ void quantize_q8_K(const GemvParams & p, int8_t * xq, float * xd, int
 // ---- per-row dot products from a shared-memory weight row ------------------------------------
 template <int MT>
 __device__ __forceinline__ void dot_q8_0(const uint8_t * wrow, const GemvParams & p, const int8_t * xq,
-                                         const float * xd, float * acc) {
+                                         const float * xd, double * acc) {
     const int lane = threadIdx.x & 31;
     const int np   = p.K / 64;  // block pairs (68 bytes, 4-byte aligned)
     for (int pr = lane; pr < np; pr += 32) {
@@ -340,8 +351,8 @@ __device__ __forceinline__ void dot_q8_0(const uint8_t * wrow, const GemvParams 
                 s1 = __dp4a((int) w[15], e.z, s1);
                 s1 = __dp4a((int) w[16], e.w, s1);
                 const float * dx = xd + m * (p.K / 32) + 2 * pr;
-                acc[m]           = __fadd_rn(acc[m], __fmul_rn((float) s0, __fmul_rn(d0, dx[0])));
-                acc[m]           = __fadd_rn(acc[m], __fmul_rn((float) s1, __fmul_rn(d1, dx[1])));
+                acc[m] += (double) __fmul_rn((float) s0, __fmul_rn(d0, dx[0]));
+                acc[m] += (double) __fmul_rn((float) s1, __fmul_rn(d1, dx[1]));
             }
         }
     }
@@ -351,7 +362,7 @@ __device__ __forceinline__ void dot_q8_0(const uint8_t * wrow, const GemvParams 
 // of a superblock are combined exactly before the float scaling.
 template <int MT>
 __device__ __forceinline__ void dot_q4_K(const uint8_t * wrow, const GemvParams & p, const int8_t * xq,
-                                         const float * xd, const int * xbs, float * acc) {
+                                         const float * xd, const int * xbs, double * acc) {
     const int lane = threadIdx.x & 31;
     const int sub  = lane & 7;
     const int nsb  = p.K / 256;
@@ -412,8 +423,8 @@ __device__ __forceinline__ void dot_q4_K(const uint8_t * wrow, const GemvParams 
                 }
                 if (valid && sub == 0) {
                     const float dx = xd[m * nsb + sb];
-                    acc[m]         = __fadd_rn(acc[m], __fmul_rn(__fmul_rn(d, dx), (float) isum));
-                    acc[m]         = __fsub_rn(acc[m], __fmul_rn(__fmul_rn(dmin, dx), (float) imin));
+                    acc[m] += (double) __fmul_rn(__fmul_rn(d, dx), (float) isum);
+                    acc[m] -= (double) __fmul_rn(__fmul_rn(dmin, dx), (float) imin);
                 }
             }
         }
@@ -424,7 +435,7 @@ __device__ __forceinline__ void dot_q4_K(const uint8_t * wrow, const GemvParams 
 // dotted and the -32 offset removed with the activation's 16-element sum (exact integers).
 template <int MT>
 __device__ __forceinline__ void dot_q6_K(const uint8_t * wrow, const GemvParams & p, const int8_t * xq,
-                                         const float * xd, const int * xbs, float * acc) {
+                                         const float * xd, const int * xbs, double * acc) {
     const int lane = threadIdx.x & 31;
     const int g    = lane & 15;
     const int nsb  = p.K / 256;
@@ -468,7 +479,7 @@ __device__ __forceinline__ void dot_q6_K(const uint8_t * wrow, const GemvParams 
                     isum += __shfl_xor_sync(0xffffffffu, isum, o);
                 }
                 if (valid && g == 0) {
-                    acc[m] = __fadd_rn(acc[m], __fmul_rn(__fmul_rn(d, xd[m * nsb + sb]), (float) isum));
+                    acc[m] += (double) __fmul_rn(__fmul_rn(d, xd[m * nsb + sb]), (float) isum);
                 }
             }
         }
@@ -554,10 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
         const int       rows  = (int) ((row1 - r) < p.chunk_rows ? (row1 - r) : p.chunk_rows);
         const uint8_t * stage = stages + (int64_t) s * p.stage_bytes;
         for (int rr = warp; rr < rows; rr += kConsumerWarps) {
-            float acc[MT];
+            double acc[MT];
 #pragma unroll
             for (int m = 0; m < MT; m++) {
-                acc[m] = 0.0f;
+                acc[m] = 0.0;
             }
             const uint8_t * wrow = stage + (int64_t) rr * p.row_bytes;
             if (QT == ACB_TYPE_Q8_0) {
@@ -570,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
 #pragma unroll
             for (int m = 0; m < MT; m++) {
                 if (m < p.M) {
-                    const float v = warp_sum(acc[m]);
+                    const float v = (float) warp_sum(acc[m]);
                     if (lane == 0) {
                         const int64_t n  = r + rr;
                         float *       yp = p.y + (int64_t) m * p.y_stride + n;
@@ -630,8 +641,9 @@ __global__ void __launch_bounds__(256) q8_0_to_tiles_kernel(const uint8_t * __re
 // Tensor-core GEMV over tiled Q8_0 weights: each CTA streams a contiguous range of tiles through
 // the shared-memory ring in stages of bs K-blocks (whole tiles when K <= 2048); warp w takes
 // blocks w, w+16, ... of a stage and issues one mma.m16n8k32 (int8, int32 sums exact) per block,
-// scaling each block's sums by d_w * d_x and adding them in fp32 (ggml's vec_dot_q8_0_q8_0
-// arithmetic per block); at the end of a tile the 16 warps' partials are added in warp order.
+// scaling each block's sums by d_w * d_x (ggml's vec_dot_q8_0_q8_0 arithmetic per block) and
+// adding the terms in double; at the end of a tile the 16 warps' partials are added in double
+// and rounded to float once.
 template <int MT, int PRO>
 __global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParams p, int bs) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -644,8 +656,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParam
     const int  xq_bytes = (MT * p.K + 15) / 16 * 16;
     float *    xd       = reinterpret_cast<float *>(smem + kHdr + xq_bytes);
     const int  xd_bytes = (MT * nb * 4 + 15) / 16 * 16;
-    float *    tred     = reinterpret_cast<float *>(smem + kHdr + xq_bytes + xd_bytes);  // [16 warps][32][4]
-    const int  st_off   = (kHdr + xq_bytes + xd_bytes + kConsumerWarps * 32 * 4 * 4 + 127) / 128 * 128;
+    double *   tred     = reinterpret_cast<double *>(smem + kHdr + xq_bytes + xd_bytes);  // [16 warps][32][4]
+    const int  st_off   = (kHdr + xq_bytes + xd_bytes + kConsumerWarps * 32 * 4 * 8 + 127) / 128 * 128;
     uint8_t *  stages   = smem + st_off;
 
     const int64_t n_tiles = p.N / 16;
@@ -693,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParam
     // this lane's batch column of the B operand (n = g) and of the accumulators (n = 2q, 2q + 1)
     const int8_t * xb  = xq + (int64_t) (g < MT ? g : 0) * p.K;
     const bool     bok = g < p.M;
-    float          acc[4] = { 0.0f, 0.0f, 0.0f, 0.0f };  // (row g, n 2q), (g, 2q+1), (g+8, 2q), (g+8, 2q+1)
+    double         acc[4] = { 0.0, 0.0, 0.0, 0.0 };  // (row g, n 2q), (g, 2q+1), (g+8, 2q), (g+8, 2q+1)
     for (int i = 0; i < nstage; i++) {
         const int s = i % p.stages;
         if (!ptx::mbar_wait(&full[s], (i / p.stages) & 1)) {
@@ -720,7 +732,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParam
                     const float dx = xd[n * nb + b];
 #pragma unroll
                     for (int r = 0; r < 2; r++) {
-                        acc[2 * r + j] = __fadd_rn(acc[2 * r + j], __fmul_rn((float) c[2 * r + j], __fmul_rn(dr[r], dx)));
+                        acc[2 * r + j] += (double) __fmul_rn((float) c[2 * r + j], __fmul_rn(dr[r], dx));
                     }
                 }
             }
@@ -731,16 +743,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParam
         }
         if (part == parts - 1) {
             // tile complete: add the 16 warps' partials in warp order and store
-            *reinterpret_cast<float4 *>(tred + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            reinterpret_cast<double2 *>(tred + (warp * 32 + lane) * 4)[0] = make_double2(acc[0], acc[1]);
+            reinterpret_cast<double2 *>(tred + (warp * 32 + lane) * 4)[1] = make_double2(acc[2], acc[3]);
             asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
             if (warp == 0) {
-                float v[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+                double v[4] = { 0.0, 0.0, 0.0, 0.0 };
                 for (int w = 0; w < kConsumerWarps; w++) {
-                    const float4 t = *reinterpret_cast<const float4 *>(tred + (w * 32 + lane) * 4);
-                    v[0]           = __fadd_rn(v[0], t.x);
-                    v[1]           = __fadd_rn(v[1], t.y);
-                    v[2]           = __fadd_rn(v[2], t.z);
-                    v[3]           = __fadd_rn(v[3], t.w);
+                    const double2 t0 = reinterpret_cast<const double2 *>(tred + (w * 32 + lane) * 4)[0];
+                    const double2 t1 = reinterpret_cast<const double2 *>(tred + (w * 32 + lane) * 4)[1];
+                    v[0] += t0.x;
+                    v[1] += t0.y;
+                    v[2] += t1.x;
+                    v[3] += t1.y;
                 }
                 const int64_t tile = t0 + i / parts;
 #pragma unroll
@@ -751,14 +765,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tiles_kernel(const GemvParam
                         if (n < p.M) {
                             const int64_t row = tile * 16 + g + 8 * r;
                             float *       yp  = p.y + (int64_t) n * p.y_stride + row;
-                            const float   val = v[2 * r + j];
+                            const float   val = (float) v[2 * r + j];
                             *yp = p.epilogue == EPI_ADD ? __fadd_rn(p.res[(int64_t) n * p.res_stride + row], val) : val;
                         }
                     }
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32));
-            acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+            acc[0] = acc[1] = acc[2] = acc[3] = 0.0;
         }
     }
 }
@@ -781,7 +795,7 @@ static acb_status launch_gemv_tiles(GemvParams p, bool pdl, cudaStream_t st) {
     p.stage_bytes         = bs * kTileBytes;
     const int xq_bytes = (MT * p.K + 15) / 16 * 16;
     const int xd_bytes = (MT * nb * 4 + 15) / 16 * 16;
-    const int st_off   = (kHdr + xq_bytes + xd_bytes + kConsumerWarps * 32 * 4 * 4 + 127) / 128 * 128;
+    const int st_off   = (kHdr + xq_bytes + xd_bytes + kConsumerWarps * 32 * 4 * 8 + 127) / 128 * 128;
     const int64_t nstage = per_cta * (nb / bs);
     int           stages = nstage < 6 ? (int) nstage : 6;
     const int64_t smem_cap = nstage > 4 ? 200 * 1024 : 110 * 1024;

@@ -141,7 +141,7 @@ acb_status enqueue_layers(acb_qw3lm * m, int n, int set0, int set_per_tok) {
         const int ns = m->splits(n);
         ACB_TRY(acb_attn_decode(m->q.as<float>(), qd, n, c.n_heads, c.n_kv_heads, D, m->pos.as<int32_t>(), kc, vc,
                                 c.max_seq_len, set0, set_per_tok, 1.0f / sqrtf((float) D), ns, m->scores.as<float>(),
-                                m->smax.as<float>(), m->part.as<float>(), m->att.as<float>(), qd,
+                                m->smax.as<float>(), m->part.as<double>(), m->att.as<float>(), qd,
                                 m->tickets.as<int>(), ACB_FLAG_PDL, (acb_stream_t) m->st));
         ACB_TRY(gemv_rows(m, L.o, 0, H, n, ACB_PRO_X, m->att.as<float>(), qd, nullptr, 0, hid, H, ACB_EPI_ADD, hid, H));
         const float * pn = (const float *) L.post_norm->data;
@@ -501,7 +501,7 @@ extern "C" acb_status acb_qw3lm_load(const char * gguf_path, int max_seq_len, in
     f |= m->q.alloc(T * m->qd() * 4) != ACB_OK;
     f |= m->scores.alloc(T * c.n_heads * (size_t) S * 4) != ACB_OK;
     f |= m->smax.alloc(T * c.n_heads * m->max_split * 4) != ACB_OK;
-    f |= m->part.alloc(part_n * m->qd() * 4) != ACB_OK;
+    f |= m->part.alloc(part_n * m->qd() * 8) != ACB_OK;  // double split partials
     f |= m->att.alloc(T * m->qd() * 4) != ACB_OK;
     f |= m->tickets.alloc(T * c.n_kv_heads * 4) != ACB_OK;  // zeroed; every attention call leaves it zero
     f |= m->gu.alloc(T * 2 * c.intermediate_size * 4) != ACB_OK;

@@ -377,7 +377,8 @@ ACB_API acb_status acb_dit_sde(float * xt, const float * vt, const float * noise
 enum {
     ACB_PRO_X          = 0, /* activation x[m][k] = x[m*x_stride + k] */
     ACB_PRO_RMSNORM    = 1, /* x = rms_norm(h[m]) * norm_w (h = x argument) */
-    ACB_PRO_SUM_SPLITS = 2, /* x[m][k] = sum_s x[(m*n_split + s)*K + k] (attention split partials) */
+    ACB_PRO_SUM_SPLITS = 2, /* x[m][k] = (float) sum_s xd[(m*n_split + s)*K + k]: x points at DOUBLE
+                               partials xd (acb_attn_decode's), added in double, rounded once */
     ACB_PRO_SWIGLU     = 3, /* x[m][k] = silu(g[m][k]) * g[m][K + k], g rows of 2K at x_stride */
 };
 enum {
@@ -393,8 +394,10 @@ enum {
  * elements in Q8_0, Q4_K or Q6_K (K a multiple of 256; W 16-byte aligned and readable up to the
  * next 16-byte boundary past its last row). The activation is quantised in-kernel to the
  * weight's ggml vec-dot type (Q8_0 / Q8_K) and dotted with integer arithmetic, exactly like
- * ggml-CPU's quantised mul_mat; `prologue` fuses the producer of x and `epilogue` the residual
- * add. Replaces ggml_mul_mat at every decode linear (src/qwen3-lm.h:639-651, 747-755) together
+ * ggml-CPU's quantised mul_mat: each block's term is (float)isum * (d_w * d_x) rounded to float,
+ * and a row's terms are added in double and rounded to float once, so the result does not
+ * depend on how the kernel partitions the row; `prologue` fuses the producer of x and
+ * `epilogue` the residual add. Replaces ggml_mul_mat at every decode linear (src/qwen3-lm.h:639-651, 747-755) together
  * with the ggml_rms_norm/ggml_mul before it (qwen3-lm.h:636,741), ggml_swiglu
  * (qwen3-enc.h:217) and ggml_add after it (qwen3-lm.h:730,738). */
 /* Repack GGUF Q8_0 rows [N][K] (N a multiple of 16) into 16-row tiles for acb_gemv with w_type
@@ -424,18 +427,26 @@ ACB_API acb_status acb_qkv_post(const float * qkv, int64_t qkv_stride, int64_t n
 ACB_API int acb_attn_decode_splits(int n_tok, int Nkv);
 
 /* One-token attention for n_tok sequences over the f16 cache, kv_len = pos[t] + 1, with
- * ggml-CPU semantics (q and normalised probabilities rounded to f16, softmax sum in double).
- * Scratch (device, caller-owned): scores [n_tok][Nh][max_seq] f32, smax [n_tok][Nh][n_split]
- * f32, part [n_tok][n_split][Nh*128] f32 split partials. With out (and tickets, int
- * [n_tok][Nkv], zeroed before first use and returned to zero by every call) the last split CTA
- * of each (token, kv head) sums the partials in split order into out[t*out_stride + h*128 + d];
- * with out NULL the partials are left for the O-projection's ACB_PRO_SUM_SPLITS prologue.
+ * ggml-CPU semantics (q and normalised probabilities rounded to f16, softmax sum in double):
+ *   s_j = (float)(sum_d q16_d k16_jd) * scale, sum in double (every product exact in float)
+ *   p_j = f16( acb_expf(s_j - max) * (float)(1 / sum_j acb_expf(s_j - max)) )
+ *   o_d = (float) sum_j p_j v16_jd, sum in double
+ * so the result is the same for any split count. Scratch (device, caller-owned): scores
+ * [n_tok][Nh][max_seq] f32, smax [n_tok][Nh][n_split] f32, part [n_tok][n_split][Nh*128] double
+ * split partials. With out (and tickets, int [n_tok][Nkv], zeroed before first use and
+ * returned to zero by every call) the last split CTA of each (token, kv head) adds the partials
+ * in double into out[t*out_stride + h*128 + d]; with out NULL the partials are left for the
+ * O-projection's ACB_PRO_SUM_SPLITS prologue.
  * Replaces ggml_flash_attn_ext / qwen3_attn_f32 on the cache view (src/qwen3-lm.h:705-723). */
 ACB_API acb_status acb_attn_decode(const float * q, int64_t q_stride, int n_tok, int Nh, int Nkv, int head_dim,
                                    const int32_t * pos, const uint16_t * k_cache, const uint16_t * v_cache,
                                    int max_seq, int set0, int set_per_tok, float scale, int n_split, float * scores,
-                                   float * smax, float * part, float * out, int64_t out_stride, int * tickets,
+                                   float * smax, double * part, float * out, int64_t out_stride, int * tickets,
                                    int flags, acb_stream_t stream);
+
+/* Largest `rows` acb_argmax takes. The scratch starts with one counter per possible row (a fixed
+ * 4 KB, whatever the call's shape), followed by the per-CTA partials. */
+#define ACB_ARGMAX_MAX_ROWS 1024
 
 /* Device scratch (bytes) acb_argmax needs for `rows` rows of V logits. */
 ACB_API size_t acb_argmax_scratch_bytes(int rows, int64_t V);
@@ -445,10 +456,11 @@ ACB_API size_t acb_argmax_scratch_bytes(int rows, int64_t V);
  * positions without a host round trip). With hist (requires pos_advance and hist_base) the
  * token is also recorded at hist[r*hist_stride + pos_advance[r] - hist_base[r]] (and its margin
  * in mhist when given) before the position advances. `scratch` is a 16-byte aligned device
- * buffer of acb_argmax_scratch_bytes(rows, V) bytes, zeroed before its first use and left
- * reusable by every call (its counters return to zero); calls that share a scratch buffer must
- * not overlap on the GPU. Replaces the temperature-0 branch of sample_top_k_p
- * (src/sampling.h:30-34). */
+ * buffer of acb_argmax_scratch_bytes(rows, V) bytes whose first 4 KB (the counters) are zeroed
+ * before its first use; every call returns the counters to zero, so one buffer sized for the
+ * largest (rows, V) serves calls of any smaller shape in any order. Calls that share a scratch
+ * buffer must not overlap on the GPU. rows <= ACB_ARGMAX_MAX_ROWS. Replaces the temperature-0
+ * branch of sample_top_k_p (src/sampling.h:30-34). */
 ACB_API acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids, float * margin,
                               int32_t * pos_advance, int32_t * hist, float * mhist, int64_t hist_stride,
                               const int32_t * hist_base, void * scratch, int flags, acb_stream_t stream);
@@ -457,14 +469,16 @@ ACB_API acb_status acb_argmax(const float * logits, int64_t stride, int64_t V, i
  * pool owns the whole device and forbids allocations it did not make, or a decode thread that
  * must never call cudaMalloc because it can synchronise the device. No counterpart in the
  * reference (which samples on the host). Same arguments and results as acb_argmax without
- * `scratch`: the scratch is a fixed array in the library's device memory, sized for
+ * `scratch`: the scratch is a fixed array in the library's device memory (64.25 KB), sized for
  * ACB_ARGMAX_NOALLOC_MAX_ROWS rows of any vocabulary, which every device that loads the
  * library holds until the process exits. More rows return ACB_ERR_UNSUPPORTED (message in
  * acb_last_error) without launching anything. Nothing is allocated by the call. The first call
- * on each device looks up the array's device address and clears it, so make that first call
- * outside any stream capture; afterwards every call leaves the array reusable. All calls on a
- * device share the array: calls that overlap on the GPU (different streams, no ordering) race
- * and must be serialised by the caller. */
+ * on each device looks up the array's device address and clears its counters with an
+ * asynchronous memset on the caller's stream, so make that first call outside any stream
+ * capture; afterwards calls of any shape, in any order, leave the array reusable. All calls on
+ * a device share the array: calls that overlap on the GPU (different streams, no ordering) race
+ * and must be serialised by the caller. The device address is cached per device ordinal for the
+ * life of the process: do not use this entry point again after cudaDeviceReset. */
 #define ACB_ARGMAX_NOALLOC_MAX_ROWS 32
 ACB_API acb_status acb_argmax_noalloc(const float * logits, int64_t stride, int64_t V, int rows, int32_t * ids,
                                       float * margin, int32_t * pos_advance, int32_t * hist, float * mhist,

@@ -5,6 +5,7 @@
  * Built with -O2 -ffp-contract=off so that no multiply-add is fused behind our back.
  */
 #include "acb_oracle.h"
+#include "../hbd-acestep.cpp_b200/csrc/acb_exp.h"
 
 #include <math.h>
 #include <stdlib.h>
@@ -559,7 +560,9 @@ void orc_qk_norm_rope(const float * x, int64_t x_tok_stride, float * y, int64_t 
 }
 
 /* ggml_swiglu / ggml_swiglu_split (qwen3-enc.h:217,221; dit-graph.h:259,264):
- * silu(g) = g / (1 + expf(-g)), times u. */
+ * silu(g) = g / (1 + exp(-g)), times u. exp is acb_expf (acb_exp.h), the library's own
+ * exponential: ggml-CPU's vectorised exp is not available here, so the oracle fixes one exp that
+ * the kernels share bit for bit. */
 void orc_swiglu(const float * g, int64_t g_stride, const float * u, int64_t u_stride, float * out, int64_t rows,
                 int64_t F) {
 #pragma omp parallel for schedule(static)
@@ -568,7 +571,7 @@ void orc_swiglu(const float * g, int64_t g_stride, const float * u, int64_t u_st
         const float * ur = u + r * u_stride;
         float *       o  = out + r * F;
         for (int64_t i = 0; i < F; i++) {
-            float s = gr[i] / (1.0f + expf(-gr[i]));
+            float s = gr[i] / (1.0f + acb_expf(-gr[i]));
             o[i]    = s * ur[i];
         }
     }
@@ -617,8 +620,14 @@ void orc_gated_residual(const float * r, const float * o, const float * gate, in
 
 /* ---- quantized mul_mat (ggml_mul_mat at every linear: qwen3-enc.h:86-88; dit-graph.h:36-49) ---- */
 
+/* The quantised dot products. Each block's term is formed in float exactly as ggml forms it
+ * (integer block dot, then (float)isum * (d_w * d_x), each product rounded), and the terms are
+ * added in double with one rounding to float at the end. ggml's own float order over the
+ * blocks depends on its SIMD width and cannot be known here; a double sum of float terms is
+ * exact whenever the terms span fewer than ~20 binades, so it gives the same float in any
+ * order and every GPU partition of the sum reproduces it. */
 static float dot_q8_0_q8_0(const uint8_t * w, const uint8_t * xq, int64_t nb) {
-    float sumf = 0.0f;
+    double sumf = 0.0;
     for (int64_t b = 0; b < nb; b++) {
         const uint8_t * wb   = w + b * 34;
         const uint8_t * xb   = xq + b * 34;
@@ -627,13 +636,13 @@ static float dot_q8_0_q8_0(const uint8_t * w, const uint8_t * xq, int64_t nb) {
             sumi += (int) (int8_t) wb[2 + j] * (int) (int8_t) xb[2 + j];
         }
         float dd = orc_f16_to_f32(rd16(wb)) * orc_f16_to_f32(rd16(xb));
-        sumf += (float) sumi * dd;
+        sumf += (double) ((float) sumi * dd);
     }
-    return sumf;
+    return (float) sumf;
 }
 
 static float dot_q4_K_q8_K(const uint8_t * w, const uint8_t * xq, int64_t nb) {
-    float sumf = 0.0f;
+    double sumf = 0.0;
     for (int64_t b = 0; b < nb; b++) {
         const uint8_t * wb = w + b * 144;
         const uint8_t * xb = xq + b * 292;
@@ -657,14 +666,14 @@ static float dot_q4_K_q8_K(const uint8_t * w, const uint8_t * xq, int64_t nb) {
         }
         float d    = orc_f16_to_f32(rd16(wb)) * dx;
         float dmin = orc_f16_to_f32(rd16(wb + 2)) * dx;
-        sumf += d * (float) isum;
-        sumf -= dmin * (float) imin;
+        sumf += (double) (d * (float) isum);
+        sumf -= (double) (dmin * (float) imin);
     }
-    return sumf;
+    return (float) sumf;
 }
 
 static float dot_q6_K_q8_K(const uint8_t * w, const uint8_t * xq, int64_t nb) {
-    float sumf = 0.0f;
+    double sumf = 0.0;
     for (int64_t b = 0; b < nb; b++) {
         const uint8_t * wb = w + b * 210;
         const uint8_t * xb = xq + b * 292;
@@ -681,9 +690,9 @@ static float dot_q6_K_q8_K(const uint8_t * w, const uint8_t * xq, int64_t nb) {
             isum += sc[g] * dot;
         }
         float d = orc_f16_to_f32(rd16(wb + 208)) * dx;
-        sumf += d * (float) isum;
+        sumf += (double) (d * (float) isum);
     }
-    return sumf;
+    return (float) sumf;
 }
 
 static int g_mm_mode = ORC_MM_GGML;
@@ -822,15 +831,18 @@ void orc_attention(const float * q, int64_t q_tok_stride, const void * k, const 
                 float x = q[i * q_tok_stride + (int64_t) h * D + d];
                 qv[d]   = f16 ? orc_f16_to_f32(orc_f32_to_f16(x)) : x;
             }
-            /* scores = K . q, then soft_max_ext: x*scale + mask */
+            /* scores = K . q, then soft_max_ext: x*scale + mask. Dot products and the P.V sums
+             * accumulate in double and round once (on the f16 cache every product is exact in
+             * float, so the sum is exact in any order unless its terms span ~24 binades); the
+             * exponential is acb_expf. */
             float mx = -INFINITY;
             for (int64_t j = 0; j < Skv; j++) {
-                float acc = 0.0f;
+                double acc = 0.0;
                 for (int d = 0; d < D; d++) {
                     float kk = kv_at(k, kv_type, j * kv_tok_stride + (int64_t) hk * kv_head_stride + d);
-                    acc += kk * qv[d];
+                    acc += f16 ? (double) (kk * qv[d]) : (double) kk * (double) qv[d];
                 }
-                float sv = acc * scale;
+                float sv = (float) acc * scale;
                 if (mask) {
                     sv = sv + mask[i * Skv + j];
                 }
@@ -839,7 +851,7 @@ void orc_attention(const float * q, int64_t q_tok_stride, const void * k, const 
             }
             double sum = 0.0;
             for (int64_t j = 0; j < Skv; j++) {
-                float e = (mx == -INFINITY) ? 0.0f : expf(s[j] - mx);
+                float e = (mx == -INFINITY) ? 0.0f : acb_expf(s[j] - mx);
                 s[j]    = e;
                 sum += (double) e;
             }
@@ -850,11 +862,12 @@ void orc_attention(const float * q, int64_t q_tok_stride, const void * k, const 
             }
             float * o = out + i * out_tok_stride + (int64_t) h * D;
             for (int d = 0; d < D; d++) {
-                float acc = 0.0f;
+                double acc = 0.0;
                 for (int64_t j = 0; j < Skv; j++) {
-                    acc += kv_at(v, kv_type, j * kv_tok_stride + (int64_t) hk * kv_head_stride + d) * s[j];
+                    float vv = kv_at(v, kv_type, j * kv_tok_stride + (int64_t) hk * kv_head_stride + d);
+                    acc += f16 ? (double) (vv * s[j]) : (double) vv * (double) s[j];
                 }
-                o[d] = acc;
+                o[d] = (float) acc;
             }
             free(s);
         }

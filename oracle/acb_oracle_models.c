@@ -3,6 +3,7 @@
  * only; see acb_oracle_models.h for the reference functions each one restates).
  */
 #include "acb_oracle_models.h"
+#include "../hbd-acestep.cpp_b200/csrc/acb_exp.h"
 
 #include <math.h>
 #include <stdlib.h>
@@ -42,8 +43,9 @@ static void add_inplace(float * h, const float * o, int64_t n) {
     }
 }
 
+/* ggml_silu with the library's exponential (acb_exp.h), like every SiLU of the oracle */
 static inline float silu(float x) {
-    return x / (1.0f + expf(-x));
+    return x / (1.0f + acb_expf(-x));
 }
 
 /* ---------------------------------------------------------------------------------------- */

@@ -34,7 +34,8 @@ def make_tensors(cfg, policy, seed=0, std=0.02, embed_std=None, prefix="model.")
 
     def mat(name, N, K, layer, s=std):
         qt = policy(name, layer, L)
-        w = (rng.standard_normal((N, K)) * s).astype(np.float32)
+        w = rng.standard_normal((N, K), dtype=np.float32)
+        w *= np.float32(s)
         out[name] = (qt, O.quantize(w, qt), K, N)
 
     def gain(name, n):
