@@ -19,7 +19,7 @@ HEADER_DIR = os.path.join(ROOT, "include")
 F32, F16, Q8_0, Q4_K, Q6_K, Q8_K, I32, BF16 = 0, 1, 8, 12, 14, 15, 26, 30
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error", 4: "out of range", 5: "oom",
-          6: "io", 7: "format", 8: "device error flag"}
+          6: "io", 7: "format", 8: "device error flag", 9: "cancelled"}
 
 
 class AcbError(RuntimeError):
@@ -108,6 +108,9 @@ def lib():
             "acb_dit_forward": (I, [P, P, P, I, I, I, F, F, P, I, P]),
             "acb_dit_generate": (I, [P, P, P, P, I, I, I, I, P, P, F, P]),
             "acb_dit_generate_solver": (I, [P, P, P, P, I, I, I, I, P, P, F, I, P]),
+            "acb_dit_generate_ex": (I, [P, P, P, P, I, I, I, I, P, P, F, P, I, P, P, P, P, P, P, P, I, F, F,
+                                        C.c_char_p, C.c_char_p, I, P, P, P]),
+            "acb_dit_set_lengths": (I, [P, P, P, P]),
             "acb_dit_free": (None, [P]),
             "acb_dit_set_condition": (I, [P, P, I, I, I, P]),
             "acb_attn_tc": (I, [P, I64, P, I64, P, I64, P, I, I64, I, I, I, I, I, I, I, I, I, F, I, I64, I64, I64, P,
@@ -721,6 +724,54 @@ class DiT:
         return out
 
     SOLVERS = {"euler": 0, "dpm3m": 1}
+
+    def set_lengths(self, real_S=None, real_enc_S=None, stream=None):
+        """Padding of the set_condition / eval path: one real length per slot (host ints)."""
+        np = self.np
+        rs = None if real_S is None else np.ascontiguousarray(real_S, dtype=np.int32)
+        re = None if real_enc_S is None else np.ascontiguousarray(real_enc_S, dtype=np.int32)
+        _check("acb_dit_set_lengths", lib().acb_dit_set_lengths(
+            self.h, None if rs is None else rs.ctypes.data, None if re is None else re.ctypes.data, _stream(stream)))
+
+    def generate_ex(self, noise, context, enc, schedule, guidance_scale=1.0, solver="euler", real_S=None,
+                    real_enc_S=None, seeds=None, randn=None, cancel=None, context_switch=None, cover_steps=-1,
+                    enc_switch=None, real_enc_S_switch=None, dcw_scaler=0.0):
+        """acb_dit_generate_ex (dit_ggml_generate's argument list). randn(seed, n) -> n floats is
+        the SDE noise source; cancel(step_count) -> bool is polled before every step. Returns
+        (x0, device ms); raises AcbError with status 9 when cancelled."""
+        np = self.np
+        f32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+        i32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.int32)
+        ptr = lambda a: None if a is None else a.ctypes.data
+        noise, context, enc = f32(noise), f32(context), f32(enc)
+        cs, es = f32(context_switch), f32(enc_switch)
+        rs, re, res = i32(real_S), i32(real_enc_S), i32(real_enc_S_switch)
+        sd = None if seeds is None else np.ascontiguousarray(seeds, dtype=np.int64)
+        sched = np.ascontiguousarray(schedule, dtype=np.float32)
+        N, T, _ = noise.shape
+        out = np.empty_like(noise)
+        ms = C.c_float(0.0)
+        CANCEL = C.CFUNCTYPE(C.c_int, C.c_void_p)
+        RANDN = C.CFUNCTYPE(None, C.c_int64, C.POINTER(C.c_float), C.c_int, C.c_void_p)
+        calls = [0]
+
+        def _cancel(_):
+            calls[0] += 1
+            return 1 if cancel(calls[0] - 1) else 0
+
+        def _randn(seed, outp, n, _):
+            v = np.ascontiguousarray(randn(int(seed), int(n)), dtype=np.float32)
+            C.memmove(outp, v.ctypes.data, 4 * int(n))
+
+        cb_c = CANCEL(_cancel) if cancel is not None else None
+        cb_r = RANDN(_randn) if randn is not None else None
+        _check("acb_dit_generate_ex", lib().acb_dit_generate_ex(
+            self.h, noise.ctypes.data, context.ctypes.data, enc.ctypes.data, enc.shape[1], T, N, sched.size,
+            sched.ctypes.data, out.ctypes.data, float(guidance_scale), ptr(cs), int(cover_steps),
+            C.cast(cb_c, C.c_void_p) if cb_c else None, None, ptr(rs), ptr(re), ptr(es), ptr(res), ptr(sd), 1,
+            float(dcw_scaler), 0.0, b"low", solver.encode() if solver else None, 10,
+            C.cast(cb_r, C.c_void_p) if cb_r else None, None, C.cast(C.pointer(ms), C.c_void_p)))
+        return out, ms.value
 
     def generate(self, noise, context, enc, schedule, guidance_scale=1.0, solver="euler"):
         """Host arrays: noise [N, T, Oc], context [N, T, in-Oc], enc [N, enc_S, enc_hidden] ->

@@ -22,6 +22,10 @@
 //               (and the O row is rescaled, each thread its 64 columns) only when the block max
 //               exceeds it by more than 2^8, so P <= 256; P written over the block's S as f16; at
 //               the end O divided by the row sum and stored.
+// Padding (dit_ggml_generate's masks, dit-sampler.h:244-304): per batch element, only keys below
+// kv_len[b] take part (key blocks past it are not loaded) and query rows from q_len[b] on are
+// written as zeros -- a row whose keys are all masked has an empty sum, which ggml's flash
+// attention turns into a zero output.
 // SPLIT: every operand comes as f16 hi and lo planes (hi + lo = the f32 value) and each product is
 // lo.hi + hi.lo + hi.hi, P split the same way -- f32-accurate attention (the reference CPU build's
 // qwen3_attn_f32 / dit_attn_f32). Every wait is bounded; on a timeout the kernel records
@@ -51,6 +55,8 @@ struct AttnTcArgs {
     int *   err;
     int     gemm_a;  // 16-bit output as [hi | hi | lo] planes Nh*128 columns apart
     int64_t o_k;     // Nh*128
+    const int * q_len;   // [batch] real query rows, or NULL (all Sq)
+    const int * kv_len;  // [batch] real keys, or NULL (all Skv)
 };
 
 template <bool SPLIT> struct TcLayout {
@@ -151,7 +157,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         kb_lo = max(0, (q0 - a.window) / kTcBK);
         kb_hi = min(kb_hi, (min(q0 + kTcBQ, a.Sq) - 1 + a.window) / kTcBK + 1);
     }
-    const int nblk = kb_hi > kb_lo ? kb_hi - kb_lo : 0;
 
     if (threadIdx.x == 0) {
         abort_flag = 0;
@@ -186,6 +191,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     ptx::grid_dep_wait();
+    // padding: the real keys and query rows of this batch element (read after the dependency
+    // wait, like every input)
+    const int klen = a.kv_len ? max(0, min(__ldg(a.kv_len + b), a.Skv)) : a.Skv;
+    const int qlen = a.q_len ? max(0, min(__ldg(a.q_len + b), a.Sq)) : a.Sq;
+    kb_hi          = min(kb_hi, (klen + kTcBK - 1) / kTcBK);
+    const int nblk = (kb_hi > kb_lo && q0 < qlen) ? kb_hi - kb_lo : 0;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -383,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tmem_ld32(tS + (uint32_t) (hf * 64 + 32), r + 32);
             const int key0 = (kb_lo + i) * kTcBK + hf * 64;
             // the mask, only on a block that crosses a boundary for this row
-            bool need = key0 + 64 > a.Skv;
+            bool need = key0 + 64 > klen;
             if (MASK == TC_MASK_CAUSAL) {
                 need = need || key0 + 63 > iq + a.causal_off;
             } else if (MASK == TC_MASK_WINDOW) {
@@ -393,7 +404,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 64; c++) {
                     const int j  = key0 + c;
-                    bool      in = j < a.Skv;
+                    bool      in = j < klen;
                     if (MASK == TC_MASK_CAUSAL) {
                         in = in && j <= iq + a.causal_off;
                     } else if (MASK == TC_MASK_WINDOW) {
@@ -507,7 +518,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             ok = pair_xchg(nblk, l, &lo_sum);
         }
         const float lt  = ok ? l + lo_sum : 0.0f;
-        const float inv = (ok && lt > 0.0f) ? 1.0f / lt : 0.0f;
+        const float inv = (ok && lt > 0.0f && iq < qlen) ? 1.0f / lt : 0.0f;
         // O rows through this warp's staging block in the (now idle) K ring, then written as whole
         // row segments: f32, or 16-bit (Q8_0: each 32 columns one block of the output projection's
         // quantised operand, ggml from_float: d = amax / 127 stored as f16, q = round(y / d))
@@ -673,11 +684,12 @@ extern "C" acb_status acb_attn_vt(const void * v, int v_type, int64_t v_bs, int6
     return launch_status();
 }
 
-extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, int64_t k_ts, const void * vt,
-                                  int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv,
-                                  int Nh, int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
-                                  int flags, int64_t q_lo, int64_t k_lo, int64_t vt_lo, int * err_flag,
-                                  acb_stream_t stream) {
+extern "C" acb_status acb_attn_tc_masked(const void * q, int64_t q_ts, const void * k, int64_t k_ts,
+                                         const void * vt, int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch,
+                                         int Sq, int Skv, int Nh, int Nkv, int head_dim, int mask, int window,
+                                         int causal_off, float scale, int flags, int64_t q_lo, int64_t k_lo,
+                                         int64_t vt_lo, const int * q_len, const int * kv_len, int * err_flag,
+                                         acb_stream_t stream) {
     if (!q || !k || !vt || !o || batch <= 0 || Sq <= 0 || Skv <= 0 || Nh <= 0 || Nkv <= 0 || Nh % Nkv != 0 ||
         vt_ld < Skv) {
         return ACB_ERR_INVALID_ARG;
@@ -734,6 +746,8 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
     a.err        = err_flag;
     a.gemm_a     = gemm_a ? 1 : 0;
     a.o_k        = (int64_t) Nh * kTcD;
+    a.q_len      = q_len;
+    a.kv_len     = kv_len;
     const size_t smem = (size_t) (split ? TcLayout<true>::TOTAL : TcLayout<false>::TOTAL) + 1024 + 256;
     void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                  const CUtensorMap, const AttnTcArgs) = nullptr;
@@ -763,4 +777,13 @@ extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, 
         return ACB_ERR_CUDA;
     }
     return ACB_OK;
+}
+
+extern "C" acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, int64_t k_ts, const void * vt,
+                                  int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv,
+                                  int Nh, int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
+                                  int flags, int64_t q_lo, int64_t k_lo, int64_t vt_lo, int * err_flag,
+                                  acb_stream_t stream) {
+    return acb_attn_tc_masked(q, q_ts, k, k_ts, vt, vt_ld, o, o_type, o_ts, batch, Sq, Skv, Nh, Nkv, head_dim, mask,
+                              window, causal_off, scale, flags, q_lo, k_lo, vt_lo, nullptr, nullptr, err_flag, stream);
 }

@@ -12,8 +12,10 @@
 //     adaLN(h, mlp_norm, scale_ff, shift_ff) -> gate||up -> SwiGLU -> down, h += o * gate_ff
 //   adaLN(h, norm_out, out_scale, out_shift) -> proj_out + bias -> velocity [Ng][T][out_ch]
 // Linears are tensor-core GEMMs (dense.h; exact mode by default). The generate loop
-// (dit_ggml_generate) runs each denoise step -- embeddings, every layer, CFG/APG, the Euler
-// update -- as one captured CUDA graph; the host only uploads t for the step.
+// (dit_ggml_generate) runs each denoise step -- embeddings, every layer, CFG/APG, the solver
+// update -- as one captured CUDA graph; the host only uploads t for the step (and, for the SDE
+// solver, the step's fresh noise). Padding: per-slot real patch positions (sa_len) and real
+// condition rows (ca_len) live in device arrays that the attention kernels read when they run.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -71,6 +73,7 @@ struct acb_dit {
     DevBuf tt, sinus, th1, th2, temb2, tproj2, ada, out_ss;
     DevBuf input, h, xn, xq, qkv32, qkv16, planes, vtb, q16, k16, att, gu, vel, pos, rope, ws, err;
     DevBuf enc_in, enc_h, kv32, kvcache;  // condition: raw [Ng][enc_S][H_enc], embedded, per-layer K / V^T planes
+    DevBuf sa_len, ca_len;                // [Ng] real patch positions / condition rows per slot
     // cached condition of one layer: K hi, K lo ([Ng*enc_S][KD] each), V^T hi, V^T lo
     // ([Ng][Nkv][128][enc_ld] each)
     size_t k_plane = 0, vt_plane = 0, kv_layer_elems = 0;
@@ -79,6 +82,7 @@ struct acb_dit {
     // generate
     DevBuf                          xt, vt, out, ra;
     DevBuf                          hist1, hist2;  // DPM++ 3M velocity history (previous, the one before)
+    DevBuf                          noise;         // SDE: the step's fresh noise [N][T][out_ch]
     std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
 
     ~acb_dit() {
@@ -107,7 +111,27 @@ struct acb_dit {
     acb_status condition(cudaStream_t s);
     acb_status evaluate(int n_layers_run, cudaStream_t s);
     acb_status layer(int l, cudaStream_t s);
+    // per-slot lengths for the Ng slots: real_S / real_enc_S of the first n slots (NULL: all real),
+    // repeated over the slots after them (the CFG twins); enqueued on s
+    acb_status set_lengths(const int * real_S, const int * real_enc_S, int n, cudaStream_t s);
 };
+
+acb_status acb_dit::set_lengths(const int * real_S, const int * real_enc_S, int n, cudaStream_t s) {
+    if (Ng <= 0 || n <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    std::vector<int> v(2 * (size_t) Ng);
+    for (int b = 0; b < Ng; b++) {
+        v[(size_t) b]      = real_S ? std::max(0, std::min(real_S[b % n], S)) : S;
+        v[(size_t) Ng + b] = real_enc_S ? std::max(0, std::min(real_enc_S[b % n], enc_S)) : enc_S;
+    }
+    // pageable source: the call returns once the values are staged, so v may go out of scope
+    if (cudaMemcpyAsync(sa_len.p, v.data(), (size_t) Ng * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        cudaMemcpyAsync(ca_len.p, v.data() + Ng, (size_t) Ng * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
 
 // ---- scratch ---------------------------------------------------------------------------------------
 
@@ -154,6 +178,8 @@ acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
     vt_plane       = (size_t) Ng * KD * enc_ld;
     kv_layer_elems = 2 * (k_plane + vt_plane);
     A(kvcache, (size_t) c.n_layers * kv_layer_elems * 2);
+    A(sa_len, (size_t) Ng * 4);
+    A(ca_len, (size_t) Ng * 4);
     if (!err.p) {
         A(err, 4, true);
     }
@@ -192,6 +218,12 @@ acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
         Ng = S = enc_S = 0;
         set_last_error("DiT scratch allocation failed");
         return ACB_ERR_OOM;
+    }
+    // no padding until a caller sets lengths (blocking copies: the buffers are new)
+    std::vector<int> v((size_t) Ng, S), ve((size_t) Ng, enc_S);
+    if (cudaMemcpy(sa_len.p, v.data(), (size_t) Ng * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(ca_len.p, ve.data(), (size_t) Ng * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        return ACB_ERR_CUDA;
     }
     return ACB_OK;
 }
@@ -302,8 +334,9 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
                                     (const float *) L.sa_q_norm->data, (const float *) L.sa_k_norm->data, eps,
                                     pos.as<int32_t>(), rope.as<float>(), S, S, hi, W, lo, vtb.as<uint16_t>(), s_ld, vl,
                                     kPdl | L.sa_qkv.op, e, as));
-        ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
-                            c.sliding_window, 0, scale, kPdl | ao_flags, lo, lo, vl, e, as));
+        ACB_TRY(acb_attn_tc_masked(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
+                                   c.sliding_window, 0, scale, kPdl | ao_flags, lo, lo, vl, sa_len.as<int>(),
+                                   sa_len.as<int>(), e, as));
     } else if (exact) {
         float * q32 = qkv32.as<float>();
         ACB_TRY(dense_forward(L.sa_qkv, true, hp, H, 0, R, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0, 0,
@@ -318,8 +351,9 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
                                         Nkv, (const float *) L.sa_k_norm->data, D, eps, pos.as<int32_t>(),
                                         rope.as<float>(), S, e, as));
         ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, vl, as));
-        ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
-                            c.sliding_window, 0, scale, kPdl | ao_flags, lo, lo, vl, e, as));
+        ACB_TRY(acb_attn_tc_masked(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
+                                   c.sliding_window, 0, scale, kPdl | ao_flags, lo, lo, vl, sa_len.as<int>(),
+                                   sa_len.as<int>(), e, as));
     } else {
         uint16_t * q16p = qkv16.as<uint16_t>();
         ACB_TRY(dense_forward(L.sa_qkv, false, hp, H, 0, R, q16p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
@@ -331,8 +365,9 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
                                  (const float *) L.sa_k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), S, e,
                                  as));
         ACB_TRY(acb_attn_vt(q16p + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, Ng, S, Nkv, D, vtb.p, s_ld, 0, as));
-        ACB_TRY(acb_attn_tc(q16.p, QD, k16.p, KD, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
-                            c.sliding_window, 0, scale, kPdl | ao_flags, 0, 0, 0, e, as));
+        ACB_TRY(acb_attn_tc_masked(q16.p, QD, k16.p, KD, vtb.p, s_ld, ao, ao_type, ao_ts, Ng, S, S, Nh, Nkv, D, mask,
+                                   c.sliding_window, 0, scale, kPdl | ao_flags, 0, 0, 0, sa_len.as<int>(),
+                                   sa_len.as<int>(), e, as));
     }
     if (fuse_o) {  // the attention wrote the output projection's operand
         ACB_TRY(dense_forward_operand(L.sa_o, exact, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, gate_sa, 0, R, sc, s));
@@ -379,16 +414,17 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
             ACB_TRY(acb_qk_norm_rope_planes(cq, ACB_TYPE_F32, QD, qh, QD, lo, R, Nh, (const float *) L.ca_q_norm->data,
                                             0, nullptr, D, eps, nullptr, nullptr, 0, e, as));
         }
-        ACB_TRY(acb_attn_tc(qh, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0, 0,
-                            0, scale, kPdl | co_flags, lo, (int64_t) k_plane, (int64_t) vt_plane, e, as));
+        ACB_TRY(acb_attn_tc_masked(qh, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0,
+                                   0, 0, scale, kPdl | co_flags, lo, (int64_t) k_plane, (int64_t) vt_plane, nullptr,
+                                   ca_len.as<int>(), e, as));
     } else {
         uint16_t * q16p = cq_fused ? planes.as<uint16_t>() : q16.as<uint16_t>();
         if (!cq_fused) {
             ACB_TRY(acb_qk_norm_rope(cq, ACB_TYPE_F32, QD, q16.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
                                      (const float *) L.ca_q_norm->data, eps, nullptr, nullptr, 0, e, as));
         }
-        ACB_TRY(acb_attn_tc(q16p, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D, 0,
-                            0, 0, scale, kPdl | co_flags, 0, 0, 0, e, as));
+        ACB_TRY(acb_attn_tc_masked(q16p, QD, k_hi, KD, vt_hi, enc_ld, co, co_type, co_ts, Ng, S, enc_S, Nh, Nkv, D,
+                                   0, 0, 0, scale, kPdl | co_flags, 0, 0, 0, nullptr, ca_len.as<int>(), e, as));
     }
     if (fuse_co) {
         ACB_TRY(dense_forward_operand(L.ca_o, exact, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0, sc, s));
@@ -741,6 +777,7 @@ extern "C" acb_status acb_dit_forward(acb_dit * m, const float * d_input, const 
         cudaMemcpyAsync(m->enc_in.p, d_enc, nen, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
+    ACB_TRY(m->set_lengths(nullptr, nullptr, N, s));
     ACB_TRY(m->condition(s));
     ACB_TRY(m->evaluate(n_layers_run, s));
     const size_t nv = (size_t) N * T * m->c.out_channels * 4;
@@ -765,7 +802,19 @@ extern "C" acb_status acb_dit_set_condition(acb_dit * m, const float * d_enc, in
     if (cudaMemcpyAsync(m->enc_in.p, d_enc, nen, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
+    ACB_TRY(m->set_lengths(nullptr, nullptr, N, s));
     return m->condition(s);
+}
+
+extern "C" acb_status acb_dit_set_lengths(acb_dit * m, const int * real_S, const int * real_enc_S,
+                                          acb_stream_t stream) {
+    if (!m || m->Ng <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    return m->set_lengths(real_S, real_enc_S, m->Ng, (cudaStream_t) stream);
 }
 
 extern "C" acb_status acb_dit_eval(acb_dit * m, const float * d_input, const float * tt, float * d_velocity,
@@ -817,6 +866,265 @@ extern "C" acb_status acb_dit_eval(acb_dit * m, const float * d_input, const flo
     return ACB_OK;
 }
 
+namespace {
+
+// The arguments of dit_ggml_generate (src/dit-sampler.h:132-158) that this library implements.
+struct GenArgs {
+    const float *   noise = nullptr, *context = nullptr, *enc = nullptr;
+    int             enc_S = 0, T = 0, N = 0, num_steps = 0;
+    const float *   schedule = nullptr;
+    float *         output   = nullptr;
+    float           guidance = 1.0f;
+    const float *   context_switch = nullptr;
+    int             cover_steps    = -1;
+    acb_cancel_fn   cancel         = nullptr;
+    void *          cancel_data    = nullptr;
+    const int *     real_S = nullptr, *real_enc_S = nullptr;
+    const float *   enc_switch        = nullptr;
+    const int *     real_enc_S_switch = nullptr;
+    const int64_t * seeds             = nullptr;
+    int             solver            = ACB_SOLVER_EULER;
+    acb_randn_fn    randn             = nullptr;
+    void *          randn_data        = nullptr;
+    float *         gpu_ms            = nullptr;
+};
+
+acb_status generate_impl(acb_dit * m, const GenArgs & g) {
+    const int  N = g.N, T = g.T, enc_S = g.enc_S, num_steps = g.num_steps;
+    const bool dpm = g.solver == ACB_SOLVER_DPM3M, sde = g.solver == ACB_SOLVER_SDE;
+    if (!m || !g.noise || !g.context || !g.enc || !g.schedule || !g.output || N <= 0 || T <= 0 || enc_S <= 0 ||
+        num_steps <= 0 || T % m->c.patch_size != 0 ||
+        (g.solver != ACB_SOLVER_EULER && g.solver != ACB_SOLVER_DPM3M && g.solver != ACB_SOLVER_SDE) ||
+        (sde && (!g.seeds || !g.randn))) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (cudaSetDevice(m->device) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    const acb_dit_config & c      = m->c;
+    const int              Oc     = c.out_channels;
+    const int              in_ch  = c.in_channels, ctx_ch = in_ch - Oc;
+    const int              He     = c.enc_hidden_size;
+    // CFG batching (dit-sampler.h:167-171): conditional slots [0, N), unconditional [N, 2N)
+    const bool do_cfg = g.guidance > 1.0f && m->null_emb;
+    const int  Ng     = do_cfg ? 2 * N : N;
+    ACB_TRY(m->reserve(Ng, T, enc_S));
+    cudaStream_t s     = m->st;
+    const size_t n_per = (size_t) T * Oc, n_tot = n_per * N;
+    bool         bad   = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
+                 m->ra.bytes < n_tot * 8 || (dpm && (m->hist1.bytes < n_tot * 4 || m->hist2.bytes < n_tot * 4)) ||
+                 (sde && m->noise.bytes < n_tot * 4);
+    if (bad) {
+        m->drop_graphs();  // the graphs hold these addresses
+        if (m->xt.alloc(n_tot * 4) != ACB_OK || m->vt.alloc(n_tot * 4) != ACB_OK || m->out.alloc(n_tot * 4) != ACB_OK ||
+            m->ra.alloc(n_tot * 8) != ACB_OK ||
+            (dpm && (m->hist1.alloc(n_tot * 4) != ACB_OK || m->hist2.alloc(n_tot * 4) != ACB_OK)) ||
+            (sde && m->noise.alloc(n_tot * 4) != ACB_OK)) {
+            set_last_error("DiT generate buffers allocation failed");
+            return ACB_ERR_OOM;
+        }
+    }
+    // inputs: context channels of every slot (uncond mirrors cond), the noise, the condition
+    std::vector<float> nul;
+    if (do_cfg) {
+        // null_condition_emb broadcast over enc_S rows for the unconditional slots (:345-385)
+        if (m->null_emb->type != ACB_TYPE_F32 || m->null_emb->K * m->null_emb->N != He) {
+            set_last_error("null_condition_emb has an unexpected shape");
+            return ACB_ERR_FORMAT;
+        }
+        nul.resize((size_t) He);
+        cudaMemcpy(nul.data(), m->null_emb->data, (size_t) He * 4, cudaMemcpyDeviceToHost);
+    }
+    auto upload_context = [&](const float * ctx) -> bool {
+        std::vector<float> in((size_t) Ng * T * in_ch, 0.0f);
+        for (int b = 0; b < Ng; b++) {
+            const int src = b % N;
+            for (int t = 0; t < T; t++) {
+                memcpy(&in[((size_t) b * T + t) * in_ch], &ctx[((size_t) src * T + t) * ctx_ch], (size_t) ctx_ch * 4);
+            }
+        }
+        return cudaMemcpyAsync(m->input.p, in.data(), in.size() * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+               cudaStreamSynchronize(s) == cudaSuccess;
+    };
+    auto upload_enc = [&](const float * e) -> bool {
+        std::vector<float> enc((size_t) Ng * enc_S * He);
+        memcpy(enc.data(), e, (size_t) N * enc_S * He * 4);
+        for (int b = N; b < Ng; b++) {
+            for (int r = 0; r < enc_S; r++) {
+                memcpy(&enc[((size_t) b * enc_S + r) * He], nul.data(), (size_t) He * 4);
+            }
+        }
+        return cudaMemcpyAsync(m->enc_in.p, enc.data(), enc.size() * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+               cudaStreamSynchronize(s) == cudaSuccess;
+    };
+    // padding (dit-sampler.h:244-304): slot b < N uses track b's lengths, its CFG twin the same
+    std::vector<int> re_now((size_t) N, enc_S);
+    if (g.real_enc_S) {
+        re_now.assign(g.real_enc_S, g.real_enc_S + N);
+    }
+    auto upload_lengths = [&](const int * re_cond, const int * re_uncond) -> acb_status {
+        std::vector<int> rs((size_t) Ng), re((size_t) Ng);
+        for (int b = 0; b < Ng; b++) {
+            rs[(size_t) b] = g.real_S ? g.real_S[b % N] : m->S;
+            re[(size_t) b] = b < N ? re_cond[b] : re_uncond[b - N];
+        }
+        return m->set_lengths(rs.data(), re.data(), Ng, s);
+    };
+    if (!upload_context(g.context) || !upload_enc(g.enc) ||
+        cudaMemcpyAsync(m->xt.p, g.noise, n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    const std::vector<int> re_first = re_now;
+    ACB_TRY(upload_lengths(re_now.data(), re_first.data()));
+    ACB_TRY(m->condition(s));
+
+    // one graph per (shape, cfg, first, last, solver, history): pack xt, evaluate, guidance, then the
+    // solver step (Euler, DPM++ 3M with min(step, 2) stored velocities, SDE with the step's noise)
+    // or the last step's x0
+    auto get_graph = [&](int first, int last, int hist, cudaGraphExec_t * ex) -> acb_status {
+        uint32_t gbits = 0;  // the guidance scale is baked into the captured APG launch
+        memcpy(&gbits, &g.guidance, 4);
+        const int  stepk = (g.solver * 3 + hist) * 4 + first * 2 + last;
+        const auto key   = std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, stepk, m->exact ? 1 : 0, gbits);
+        auto       it  = m->graphs.find(key);
+        if (it != m->graphs.end()) {
+            *ex = it->second;
+            return ACB_OK;
+        }
+        cudaGraph_t gr = nullptr;
+        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        acb_status st = acb_dit_pack_xt(m->xt.as<float>(), m->input.as<float>(), N, Ng, T, Oc, ctx_ch, (acb_stream_t) s);
+        if (st == ACB_OK) {
+            st = m->evaluate(-1, s);
+        }
+        float * v = m->vel.as<float>();
+        if (st == ACB_OK && do_cfg) {
+            st = acb_dit_apg(v, v + n_tot, m->ra.as<double>(), first, -0.75f, g.guidance, 2.5f, N, T, Oc,
+                             m->vt.as<float>(), (acb_stream_t) s);
+            v  = m->vt.as<float>();
+        }
+        if (st == ACB_OK && dpm && !last) {
+            st = acb_dit_dpm3m(m->xt.as<float>(), v, m->hist1.as<float>(), m->hist2.as<float>(), hist,
+                               m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
+        } else if (st == ACB_OK && sde && !last) {
+            st = acb_dit_sde(m->xt.as<float>(), v, m->noise.as<float>(), m->tt.as<float>(), (int64_t) n_tot,
+                             (acb_stream_t) s);
+        } else if (st == ACB_OK) {
+            st = acb_dit_euler(m->xt.as<float>(), v, m->tt.as<float>(), last, m->out.as<float>(), (int64_t) n_tot,
+                               (acb_stream_t) s);
+        }
+        const cudaError_t ce = cudaStreamEndCapture(s, &gr);
+        if (st != ACB_OK || ce != cudaSuccess) {
+            if (gr) {
+                cudaGraphDestroy(gr);
+            }
+            set_last_error("DiT step graph capture failed");
+            return st != ACB_OK ? st : ACB_ERR_CUDA;
+        }
+        const cudaError_t ie = cudaGraphInstantiate(ex, gr, 0);
+        cudaGraphDestroy(gr);
+        if (ie != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        m->graphs.emplace(key, *ex);
+        return ACB_OK;
+    };
+    cudaEvent_t e0 = nullptr, e1 = nullptr, done[2] = { nullptr, nullptr };
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming);
+    acb_status         st = ACB_OK;
+    std::vector<float> tv((size_t) num_steps * 3);
+    std::vector<float> fresh(sde ? n_tot : 0);
+    bool               switched = false;
+    for (int step = 0; step < num_steps && st == ACB_OK; step++) {
+        // at most two steps in flight, so that a cancellation (polled before every step, like
+        // dit-sampler.h:409-413) takes effect within two steps
+        if (step >= 2 && cudaEventSynchronize(done[step & 1]) != cudaSuccess) {
+            st = ACB_ERR_CUDA;
+            break;
+        }
+        if (g.cancel && g.cancel(g.cancel_data)) {
+            cudaStreamSynchronize(s);
+            set_last_error("cancelled at step " + std::to_string(step) + "/" + std::to_string(num_steps));
+            st = ACB_ERR_CANCELLED;
+            break;
+        }
+        // cover mode (dit-sampler.h:414-449): from cover_steps on, the other context (every slot)
+        // and, for the conditional slots, the other condition and its lengths
+        if (g.context_switch && g.cover_steps >= 0 && step >= g.cover_steps && !switched) {
+            switched = true;
+            if (cudaStreamSynchronize(s) != cudaSuccess || !upload_context(g.context_switch)) {
+                st = ACB_ERR_CUDA;
+                break;
+            }
+            if (g.enc_switch) {
+                if (g.real_enc_S_switch) {
+                    re_now.assign(g.real_enc_S_switch, g.real_enc_S_switch + N);
+                }
+                if (!upload_enc(g.enc_switch) || upload_lengths(re_now.data(), re_first.data()) != ACB_OK ||
+                    m->condition(s) != ACB_OK) {
+                    st = ACB_ERR_CUDA;
+                    break;
+                }
+            }
+        }
+        const int       first = step == 0, last = step == num_steps - 1;
+        cudaGraphExec_t ex    = nullptr;
+        st                    = get_graph(first, last, dpm ? (step < 2 ? step : 2) : 0, &ex);
+        if (st != ACB_OK) {
+            break;
+        }
+        // SDE: the fresh noise of every track from its seed (solver-sde.h:28-31: seed_b + step + 1)
+        if (sde && !last) {
+            for (int b = 0; b < N; b++) {
+                g.randn(g.seeds[b] + step + 1, fresh.data() + (size_t) b * n_per, (int) n_per, g.randn_data);
+            }
+            if (cudaMemcpyAsync(m->noise.p, fresh.data(), n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+                st = ACB_ERR_CUDA;
+                break;
+            }
+        }
+        // t_curr, t_r = t_curr (dit-sampler.h:431-436), t_next
+        float * t3 = &tv[(size_t) step * 3];
+        t3[0]      = g.schedule[step];
+        t3[1]      = g.schedule[step];
+        t3[2]      = last ? 0.0f : g.schedule[step + 1];
+        if (step == 0) {
+            cudaEventRecord(e0, s);
+        }
+        if (cudaMemcpyAsync(m->tt.p, t3, 3 * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess ||
+            cudaGraphLaunch(ex, s) != cudaSuccess || cudaEventRecord(done[step & 1], s) != cudaSuccess) {
+            st = ACB_ERR_CUDA;
+        }
+    }
+    cudaEventRecord(e1, s);
+    int dev_err = 0;
+    if (st == ACB_OK && (cudaMemcpyAsync(g.output, m->out.p, n_tot * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                         cudaMemcpyAsync(&dev_err, m->err.p, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+                         cudaStreamSynchronize(s) != cudaSuccess)) {
+        st = ACB_ERR_CUDA;
+    }
+    cudaStreamSynchronize(s);
+    if (st == ACB_OK && g.gpu_ms) {
+        cudaEventElapsedTime(g.gpu_ms, e0, e1);
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(done[0]);
+    cudaEventDestroy(done[1]);
+    if (st == ACB_OK && dev_err) {
+        set_last_error("device error flag " + std::to_string(dev_err));
+        return ACB_ERR_DEVICE;
+    }
+    return st;
+}
+
+}  // namespace
+
 extern "C" acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
                                        const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                        const float * schedule, float * output, float guidance_scale, float * gpu_ms) {
@@ -828,162 +1136,75 @@ extern "C" acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, 
                                               const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                               const float * schedule, float * output, float guidance_scale,
                                               int solver, float * gpu_ms) {
-    if (!m || !noise || !context_latents || !enc_hidden || !schedule || !output || N <= 0 || T <= 0 || enc_S <= 0 ||
-        num_steps <= 0 || T % m->c.patch_size != 0 || (solver != ACB_SOLVER_EULER && solver != ACB_SOLVER_DPM3M)) {
-        return ACB_ERR_INVALID_ARG;
+    if (solver != ACB_SOLVER_EULER && solver != ACB_SOLVER_DPM3M) {
+        return ACB_ERR_INVALID_ARG;  // the SDE solver needs seeds and a noise source: acb_dit_generate_ex
     }
-    const bool dpm = solver == ACB_SOLVER_DPM3M;
-    if (cudaSetDevice(m->device) != cudaSuccess) {
-        return ACB_ERR_CUDA;
-    }
-    const acb_dit_config & c      = m->c;
-    const int              Oc     = c.out_channels;
-    const int              in_ch  = c.in_channels, ctx_ch = in_ch - Oc;
-    const int              He     = c.enc_hidden_size;
-    // CFG batching (dit-sampler.h:167-171): conditional slots [0, N), unconditional [N, 2N)
-    const bool do_cfg = guidance_scale > 1.0f && m->null_emb;
-    const int  Ng     = do_cfg ? 2 * N : N;
-    ACB_TRY(m->reserve(Ng, T, enc_S));
-    cudaStream_t s     = m->st;
-    const size_t n_per = (size_t) T * Oc, n_tot = n_per * N;
-    bool         bad   = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
-                 m->ra.bytes < n_tot * 8 || (dpm && (m->hist1.bytes < n_tot * 4 || m->hist2.bytes < n_tot * 4));
-    if (bad) {
-        m->drop_graphs();  // the graphs hold these addresses
-        if (m->xt.alloc(n_tot * 4) != ACB_OK || m->vt.alloc(n_tot * 4) != ACB_OK || m->out.alloc(n_tot * 4) != ACB_OK ||
-            m->ra.alloc(n_tot * 8) != ACB_OK ||
-            (dpm && (m->hist1.alloc(n_tot * 4) != ACB_OK || m->hist2.alloc(n_tot * 4) != ACB_OK))) {
-            set_last_error("DiT generate buffers allocation failed");
-            return ACB_ERR_OOM;
-        }
-    }
-    // inputs: context channels of every slot (uncond mirrors cond), the noise, the condition
-    {
-        std::vector<float> in((size_t) Ng * T * in_ch, 0.0f);
-        for (int b = 0; b < Ng; b++) {
-            const int src = b % N;
-            for (int t = 0; t < T; t++) {
-                memcpy(&in[((size_t) b * T + t) * in_ch], &context_latents[((size_t) src * T + t) * ctx_ch],
-                       (size_t) ctx_ch * 4);
-            }
-        }
-        std::vector<float> enc((size_t) Ng * enc_S * He);
-        memcpy(enc.data(), enc_hidden, (size_t) N * enc_S * He * 4);
-        if (do_cfg) {
-            // null_condition_emb broadcast over enc_S rows for the unconditional slots (:345-385)
-            std::vector<float> nul((size_t) He);
-            if (m->null_emb->type == ACB_TYPE_F32 && m->null_emb->K * m->null_emb->N == He) {
-                cudaMemcpy(nul.data(), m->null_emb->data, (size_t) He * 4, cudaMemcpyDeviceToHost);
-            } else {
-                set_last_error("null_condition_emb has an unexpected shape");
-                return ACB_ERR_FORMAT;
-            }
-            for (int b = N; b < Ng; b++) {
-                for (int r = 0; r < enc_S; r++) {
-                    memcpy(&enc[((size_t) b * enc_S + r) * He], nul.data(), (size_t) He * 4);
-                }
-            }
-        }
-        if (cudaMemcpyAsync(m->input.p, in.data(), in.size() * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaMemcpyAsync(m->enc_in.p, enc.data(), enc.size() * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaMemcpyAsync(m->xt.p, noise, n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaStreamSynchronize(s) != cudaSuccess) {
-            return ACB_ERR_CUDA;
-        }
-    }
-    ACB_TRY(m->condition(s));
+    GenArgs g;
+    g.noise     = noise;
+    g.context   = context_latents;
+    g.enc       = enc_hidden;
+    g.enc_S     = enc_S;
+    g.T         = T;
+    g.N         = N;
+    g.num_steps = num_steps;
+    g.schedule  = schedule;
+    g.output    = output;
+    g.guidance  = guidance_scale;
+    g.solver    = solver;
+    g.gpu_ms    = gpu_ms;
+    return generate_impl(m, g);
+}
 
-    // one graph per (shape, cfg, first, last, solver, history): pack xt, evaluate, guidance, then the
-    // solver step (Euler, or DPM++ 3M with min(step, 2) stored velocities) or the last step's x0
-    auto get_graph = [&](int first, int last, int hist, cudaGraphExec_t * ex) -> acb_status {
-        uint32_t gbits = 0;  // the guidance scale is baked into the captured APG launch
-        memcpy(&gbits, &guidance_scale, 4);
-        const int  stepk = ((dpm ? 1 : 0) * 3 + hist) * 4 + first * 2 + last;
-        const auto key   = std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, stepk, m->exact ? 1 : 0, gbits);
-        auto       it  = m->graphs.find(key);
-        if (it != m->graphs.end()) {
-            *ex = it->second;
-            return ACB_OK;
-        }
-        cudaGraph_t g = nullptr;
-        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-            return ACB_ERR_CUDA;
-        }
-        acb_status st = acb_dit_pack_xt(m->xt.as<float>(), m->input.as<float>(), N, Ng, T, Oc, ctx_ch, (acb_stream_t) s);
-        if (st == ACB_OK) {
-            st = m->evaluate(-1, s);
-        }
-        float * v = m->vel.as<float>();
-        if (st == ACB_OK && do_cfg) {
-            st = acb_dit_apg(v, v + n_tot, m->ra.as<double>(), first, -0.75f, guidance_scale, 2.5f, N, T, Oc,
-                             m->vt.as<float>(), (acb_stream_t) s);
-            v  = m->vt.as<float>();
-        }
-        if (st == ACB_OK && dpm && !last) {
-            st = acb_dit_dpm3m(m->xt.as<float>(), v, m->hist1.as<float>(), m->hist2.as<float>(), hist,
-                               m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
-        } else if (st == ACB_OK) {
-            st = acb_dit_euler(m->xt.as<float>(), v, m->tt.as<float>(), last, m->out.as<float>(), (int64_t) n_tot,
-                               (acb_stream_t) s);
-        }
-        const cudaError_t ce = cudaStreamEndCapture(s, &g);
-        if (st != ACB_OK || ce != cudaSuccess) {
-            if (g) {
-                cudaGraphDestroy(g);
-            }
-            set_last_error("DiT step graph capture failed");
-            return st != ACB_OK ? st : ACB_ERR_CUDA;
-        }
-        const cudaError_t ie = cudaGraphInstantiate(ex, g, 0);
-        cudaGraphDestroy(g);
-        if (ie != cudaSuccess) {
-            return ACB_ERR_CUDA;
-        }
-        m->graphs.emplace(key, *ex);
-        return ACB_OK;
-    };
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    cudaEventCreate(&e0);
-    cudaEventCreate(&e1);
-    acb_status st = ACB_OK;
-    std::vector<float> tv((size_t) num_steps * 3);
-    for (int step = 0; step < num_steps && st == ACB_OK; step++) {
-        const int       first = step == 0, last = step == num_steps - 1;
-        cudaGraphExec_t ex    = nullptr;
-        st                    = get_graph(first, last, dpm ? (step < 2 ? step : 2) : 0, &ex);
-        if (st != ACB_OK) {
-            break;
-        }
-        // t_curr, t_r = t_curr (dit-sampler.h:431-436), t_next
-        float * t3 = &tv[(size_t) step * 3];
-        t3[0]      = schedule[step];
-        t3[1]      = schedule[step];
-        t3[2]      = last ? 0.0f : schedule[step + 1];
-        if (step == 0) {
-            cudaEventRecord(e0, s);
-        }
-        if (cudaMemcpyAsync(m->tt.p, t3, 3 * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaGraphLaunch(ex, s) != cudaSuccess) {
-            st = ACB_ERR_CUDA;
-        }
+extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, const float * context_latents,
+                                          const float * enc_hidden, int enc_S, int T, int N, int num_steps,
+                                          const float * schedule, float * output, float guidance_scale,
+                                          const float * context_switch, int cover_steps, acb_cancel_fn cancel,
+                                          void * cancel_data, const int * real_S, const int * real_enc_S,
+                                          const float * enc_switch, const int * real_enc_S_switch,
+                                          const int64_t * seeds, int use_batch_cfg, float dcw_scaler,
+                                          float dcw_high_scaler, const char * dcw_mode, const char * solver_name,
+                                          int stork_substeps, acb_randn_fn randn, void * randn_data, float * gpu_ms) {
+    (void) use_batch_cfg;   // both settings run the batched graph: HBM is not the constraint here
+    (void) stork_substeps;  // STORK is not provided (see below)
+    (void) dcw_mode;
+    if (dcw_scaler > 0.0f || dcw_high_scaler > 0.0f) {
+        set_last_error("acb_dit_generate_ex: DCW (dwt-haar.h) is not provided by this library");
+        return ACB_ERR_UNSUPPORTED;
     }
-    cudaEventRecord(e1, s);
-    int dev_err = 0;
-    if (st == ACB_OK && (cudaMemcpyAsync(output, m->out.p, n_tot * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-                         cudaMemcpyAsync(&dev_err, m->err.p, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-                         cudaStreamSynchronize(s) != cudaSuccess)) {
-        st = ACB_ERR_CUDA;
+    int solver = ACB_SOLVER_EULER;  // solver_lookup: NULL or "" is euler; an unknown name falls back to it
+    if (solver_name && std::strcmp(solver_name, "dpm3m") == 0) {
+        solver = ACB_SOLVER_DPM3M;
+    } else if (solver_name && std::strcmp(solver_name, "sde") == 0) {
+        solver = ACB_SOLVER_SDE;
+    } else if (solver_name && std::strcmp(solver_name, "stork4") == 0) {
+        set_last_error("acb_dit_generate_ex: the STORK4 solver is not provided by this library");
+        return ACB_ERR_UNSUPPORTED;
     }
-    if (st == ACB_OK && gpu_ms) {
-        cudaEventElapsedTime(gpu_ms, e0, e1);
-    }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    if (st == ACB_OK && dev_err) {
-        set_last_error("device error flag " + std::to_string(dev_err));
-        return ACB_ERR_DEVICE;
-    }
-    return st;
+    GenArgs g;
+    g.noise             = noise;
+    g.context           = context_latents;
+    g.enc               = enc_hidden;
+    g.enc_S             = enc_S;
+    g.T                 = T;
+    g.N                 = N;
+    g.num_steps         = num_steps;
+    g.schedule          = schedule;
+    g.output            = output;
+    g.guidance          = guidance_scale;
+    g.context_switch    = context_switch;
+    g.cover_steps       = cover_steps;
+    g.cancel            = cancel;
+    g.cancel_data       = cancel_data;
+    g.real_S            = real_S;
+    g.real_enc_S        = real_enc_S;
+    g.enc_switch        = enc_switch;
+    g.real_enc_S_switch = real_enc_S_switch;
+    g.seeds             = seeds;
+    g.solver            = solver;
+    g.randn             = randn;
+    g.randn_data        = randn_data;
+    g.gpu_ms            = gpu_ms;
+    return generate_impl(m, g);
 }
 
 extern "C" int acb_dit_eval_kernels(const acb_dit * m) {

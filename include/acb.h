@@ -47,6 +47,7 @@ typedef enum {
     ACB_ERR_IO           = 6, /* file open / map / read failed */
     ACB_ERR_FORMAT       = 7, /* malformed or truncated GGUF, missing tensor */
     ACB_ERR_DEVICE       = 8, /* a kernel reported an error through its device flag */
+    ACB_ERR_CANCELLED    = 9, /* the caller's cancel callback asked to stop (the reference returns -1) */
 } acb_status;
 
 typedef enum {
@@ -324,6 +325,17 @@ ACB_API acb_status acb_attn_tc(const void * q, int64_t q_ts, const void * k, int
                                int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv, int Nh,
                                int Nkv, int head_dim, int mask, int window, int causal_off, float scale, int flags,
                                int64_t q_lo, int64_t k_lo, int64_t vt_lo, int * err_flag, acb_stream_t stream);
+/* acb_attn_tc with the padding masks of dit_ggml_generate (src/dit-sampler.h:244-304): for batch
+ * element b only keys j < kv_len[b] take part (with the window or causal mask on top), and query
+ * rows i >= q_len[b] are written as zeros (all their keys are masked: the empty sum of ggml's
+ * flash attention). q_len / kv_len are device int arrays [batch], read when the kernel runs (so a
+ * captured graph follows their current contents), or NULL for no padding. The DiT passes
+ * q_len = kv_len = real_S for self-attention and kv_len = real_enc_S for cross-attention. */
+ACB_API acb_status acb_attn_tc_masked(const void * q, int64_t q_ts, const void * k, int64_t k_ts, const void * vt,
+                                      int64_t vt_ld, void * o, int o_type, int64_t o_ts, int batch, int Sq, int Skv,
+                                      int Nh, int Nkv, int head_dim, int mask, int window, int causal_off, float scale,
+                                      int flags, int64_t q_lo, int64_t k_lo, int64_t vt_lo, const int * q_len,
+                                      const int * kv_len, int * err_flag, acb_stream_t stream);
 /* V (f32 or f16; element (b, t, hk, d) at b*v_bs + t*v_ts + hk*128 + d) to the transposed f16
  * operand of acb_attn_tc: vt[((b*Nkv + hk)*128 + d)*vt_ld + t]; with lo_offset nonzero also the lo
  * plane f16(v - hi) at lo_offset elements further. */

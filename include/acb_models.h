@@ -130,6 +130,11 @@ ACB_API acb_status acb_dit_set_exact(acb_dit * m, int exact);
 ACB_API acb_status acb_dit_forward(acb_dit * m, const float * d_input, const float * d_enc, int N, int T, int enc_S,
                                    float t, float t_r, float * d_velocity, int n_layers_run, acb_stream_t stream);
 
+/* Padding for the acb_dit_set_condition / acb_dit_eval path (dit-sampler.h:244-304): host arrays of
+ * the slots' real patch positions (self-attention queries and keys) and real condition rows
+ * (cross-attention keys), one value per sequence of the last acb_dit_set_condition (NULL: all
+ * real). acb_dit_set_condition and acb_dit_forward reset both to "all real". Enqueued on stream. */
+ACB_API acb_status acb_dit_set_lengths(acb_dit * m, const int * real_S, const int * real_enc_S, acb_stream_t stream);
 /* The two halves of acb_dit_forward for callers that run their own step loop (e.g. sequences
  * sharded over GPUs): set_condition embeds enc [N][enc_S][enc_hidden_size] (device) and caches
  * every layer's cross-attention K/V for N sequences of T frames; eval runs one evaluation of
@@ -147,13 +152,13 @@ ACB_API int        acb_dit_eval_kernels(const acb_dit * m);
  * [N][enc_S][enc_hidden_size], schedule[num_steps] -> output [N][T][out_channels] (the x0
  * prediction of the last step). guidance_scale > 1 with a null condition runs batched CFG
  * (2N sequences per evaluation) with APG. Each step is one CUDA graph (captured on first use per
- * shape); gpu_ms (optional) receives the device time of the step loop. Not covered: cover mode,
- * padding masks (real_S / real_enc_S), DCW and the other solvers. */
+ * shape); gpu_ms (optional) receives the device time of the step loop. The full argument list
+ * (padding masks, cancellation, cover mode, the SDE solver) is acb_dit_generate_ex. */
 ACB_API acb_status acb_dit_generate(acb_dit * m, const float * noise, const float * context_latents,
                                     const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                     const float * schedule, float * output, float guidance_scale, float * gpu_ms);
-/* Solvers of acb_dit_generate_solver (the registry keys of solvers/solver-registry.h:30-32). */
-enum { ACB_SOLVER_EULER = 0, ACB_SOLVER_DPM3M = 1 };
+/* Solvers (the registry keys of solvers/solver-registry.h:30-33: "euler", "dpm3m", "sde"). */
+enum { ACB_SOLVER_EULER = 0, ACB_SOLVER_DPM3M = 1, ACB_SOLVER_SDE = 2 };
 /* acb_dit_generate with dit_ggml_generate's solver choice (dit-sampler.h:391-398, 608-611): Euler or
  * DPM++ 3M (acb_dit_dpm3m on the velocity after guidance, its history on the device; the last
  * step is the x0 prediction for every solver). Other solver values: ACB_ERR_INVALID_ARG. */
@@ -161,6 +166,39 @@ ACB_API acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, con
                                            const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                            const float * schedule, float * output, float guidance_scale, int solver,
                                            float * gpu_ms);
+/* Cancellation callback polled before every denoise step (dit-sampler.h:409-413): nonzero stops. */
+typedef int (*acb_cancel_fn)(void * data);
+/* Noise source of the SDE solver: n N(0,1) samples of the stream seeded with `seed` into out. The
+ * reference's is philox_randn(seed, out, n, true) (src/philox.h: Philox4x32-10, rounded to bf16);
+ * a caller binding ace-synth passes that function, so trajectories match the reference's. */
+typedef void (*acb_randn_fn)(int64_t seed, float * out, int n, void * data);
+/* dit_ggml_generate (src/dit-sampler.h:132-711) argument for argument, host arrays as in the
+ * reference:
+ *   noise [N][T][Oc], context_latents [N][T][in_ch - Oc], enc_hidden [N][enc_S][enc_hidden_size],
+ *   schedule[num_steps] -> output [N][T][Oc] (x0 of the last step), guidance_scale (> 1 with a
+ *   null condition: batched CFG with APG);
+ *   context_switch / cover_steps / enc_switch / real_enc_S_switch: cover mode (:414-449): from
+ *   step cover_steps on, every slot's context is context_switch and the conditional slots'
+ *   condition is enc_switch with lengths real_enc_S_switch (the unconditional slots keep theirs);
+ *   cancel(cancel_data): polled before every step; nonzero stops with ACB_ERR_CANCELLED (at most
+ *   two steps are queued on the GPU, so it takes effect within two steps);
+ *   real_S[N] / real_enc_S[N]: padding masks (:244-304; NULL: no padding);
+ *   seeds[N] + randn / randn_data: the SDE solver's per-step noise (seed_b + step + 1);
+ *   use_batch_cfg: accepted, both values run the batched graph (results equal up to summation order);
+ *   dcw_*: DCW is not provided (dcw_scaler or dcw_high_scaler > 0: ACB_ERR_UNSUPPORTED);
+ *   solver_name: "euler" (also NULL / ""), "dpm3m", "sde"; "stork4": ACB_ERR_UNSUPPORTED; any
+ *   other name falls back to Euler, as solver_lookup's caller does;
+ *   gpu_ms (optional): device time of the step loop.
+ * Returns ACB_OK where the reference returns 0. */
+ACB_API acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, const float * context_latents,
+                                       const float * enc_hidden, int enc_S, int T, int N, int num_steps,
+                                       const float * schedule, float * output, float guidance_scale,
+                                       const float * context_switch, int cover_steps, acb_cancel_fn cancel,
+                                       void * cancel_data, const int * real_S, const int * real_enc_S,
+                                       const float * enc_switch, const int * real_enc_S_switch, const int64_t * seeds,
+                                       int use_batch_cfg, float dcw_scaler, float dcw_high_scaler,
+                                       const char * dcw_mode, const char * solver_name, int stork_substeps,
+                                       acb_randn_fn randn, void * randn_data, float * gpu_ms);
 ACB_API void       acb_dit_free(acb_dit * m);
 
 /* ---- Qwen3 causal LM (replaces src/qwen3-lm.h) ---------------------------------------------- */

@@ -324,7 +324,7 @@ int orc_dit_timestep(const orc_dit * m, const orc_dit_temb * te, float t, float 
 
 /* dit_ggml_build_layer (dit-graph.h:367-450). hidden [N][S][H], enc [N][enc_S][H]. */
 static int dit_layer(const orc_dit * m, const orc_dit_layer * ly, float * hidden, const float * enc, int N, int S,
-                     int enc_S, const float * tproj, const float * rope) {
+                     int enc_S, const float * tproj, const float * rope, const int * real_S, const int * real_enc_S) {
     const int     H = m->H, D = m->D, Nh = m->Nh, Nkv = m->Nkv, F = m->F;
     const int     qd = Nh * D, kvd = Nkv * D, qkvd = qd + 2 * kvd;
     const int64_t R  = (int64_t) N * S;
@@ -360,19 +360,26 @@ static int dit_layer(const orc_dit * m, const orc_dit_layer * ly, float * hidden
             memcpy(v + ((int64_t) b * S + s) * kvd, qb + (int64_t) s * qkvd + qd + kvd, sizeof(float) * kvd);
         }
     }
-    float * mask = NULL;
-    int     win  = m->sliding_window;
-    if (ly->layer_type == 0 && win > 0 && S > win) {
+    /* self-attention mask of sequence b (dit-sampler.h:253-282): sa_mask_sw on the sliding layers
+     * (window and padding), sa_mask_pad on the full ones (padding only) */
+    float *     mask = NULL;
+    int         win  = m->sliding_window;
+    const int   swa  = ly->layer_type == 0 && win > 0 && S > win;
+    const float scale = 1.0f / sqrtf((float) D);
+    if (swa || real_S) {
         mask = fbuf((int64_t) S * S);
-        for (int i = 0; i < S; i++) {
-            for (int j = 0; j < S; j++) {
-                int dist                  = i > j ? i - j : j - i;
-                mask[(int64_t) i * S + j] = dist <= win ? 0.0f : -INFINITY;
+    }
+    for (int b = 0; b < N; b++) {
+        if (mask) {
+            const int rs = real_S ? real_S[b] : S;
+            for (int i = 0; i < S; i++) {
+                for (int j = 0; j < S; j++) {
+                    int dist                  = i > j ? i - j : j - i;
+                    int ok                    = i < rs && j < rs && (!swa || dist <= win);
+                    mask[(int64_t) i * S + j] = ok ? 0.0f : -INFINITY;
+                }
             }
         }
-    }
-    const float scale = 1.0f / sqrtf((float) D);
-    for (int b = 0; b < N; b++) {
         orc_attention(q + (int64_t) b * S * qd, qd, k + (int64_t) b * S * kvd, v + (int64_t) b * S * kvd, ORC_F32,
                       kvd, D, mask, att + (int64_t) b * S * qd, qd, S, S, Nh, Nkv, D, scale);
     }
@@ -394,10 +401,20 @@ static int dit_layer(const orc_dit * m, const orc_dit_layer * ly, float * hidden
         for (int64_t r = 0; r < Re; r++) {
             memcpy(ve + r * kvd, kvb + r * 2 * kvd + kvd, sizeof(float) * kvd);
         }
+        /* cross-attention mask (dit-sampler.h:288-304): condition rows ki < real_enc_S[b] */
+        float * cmask = real_enc_S ? fbuf((int64_t) S * enc_S) : NULL;
         for (int b = 0; b < N; b++) {
+            if (cmask) {
+                for (int i = 0; i < S; i++) {
+                    for (int j = 0; j < enc_S; j++) {
+                        cmask[(int64_t) i * enc_S + j] = j < real_enc_S[b] ? 0.0f : -INFINITY;
+                    }
+                }
+            }
             orc_attention(q + (int64_t) b * S * qd, qd, ke + (int64_t) b * enc_S * kvd, ve + (int64_t) b * enc_S * kvd,
-                          ORC_F32, kvd, D, NULL, att + (int64_t) b * S * qd, qd, S, enc_S, Nh, Nkv, D, scale);
+                          ORC_F32, kvd, D, cmask, att + (int64_t) b * S * qd, qd, S, enc_S, Nh, Nkv, D, scale);
         }
+        free(cmask);
         rc |= linear(&ly->ca_o, att, R, o);
         add_inplace(hidden, o, R * H);
         free(kvb);
@@ -429,6 +446,12 @@ static int dit_layer(const orc_dit * m, const orc_dit_layer * ly, float * hidden
 
 int orc_dit_forward(const orc_dit * m, const float * input, const float * enc_in, int N, int T, int enc_S, float t,
                     float t_r, float * velocity, int n_layers_run) {
+    return orc_dit_forward_masked(m, input, enc_in, N, T, enc_S, t, t_r, velocity, n_layers_run, NULL, NULL);
+}
+
+int orc_dit_forward_masked(const orc_dit * m, const float * input, const float * enc_in, int N, int T, int enc_S,
+                           float t, float t_r, float * velocity, int n_layers_run, const int * real_S,
+                           const int * real_enc_S) {
     const int     H = m->H, P = m->P, S = T / P;
     const int64_t R  = (int64_t) N * S;
     int           rc = 0;
@@ -469,7 +492,7 @@ int orc_dit_forward(const orc_dit * m, const float * input, const float * enc_in
 
     int nl = n_layers_run < 0 || n_layers_run > m->n_layers ? m->n_layers : n_layers_run;
     for (int l = 0; l < nl && rc == 0; l++) {
-        rc |= dit_layer(m, &m->layers[l], hidden, enc, N, S, enc_S, tproj, rope);
+        rc |= dit_layer(m, &m->layers[l], hidden, enc, N, S, enc_S, tproj, rope, real_S, real_enc_S);
     }
 
     /* output adaLN + proj_out (dit-graph.h:588-612) */

@@ -121,6 +121,16 @@ typedef struct {
 int orc_dit_forward(const orc_dit * m, const float * input, const float * enc, int N, int T, int enc_S, float t,
                     float t_r, float * velocity, int n_layers_run);
 
+/* orc_dit_forward with the padding masks of dit_ggml_generate (dit-sampler.h:244-304): sequence b
+ * has real_S[b] real patch positions (self-attention: query and key both real, and inside the
+ * window on the sliding layers) and real_enc_S[b] real condition rows (cross-attention keys).
+ * Either array may be NULL (every position real). A query row with no admitted key (a padded
+ * position) gets a zero attention output: the masked keys are skipped and the empty sum gives 0,
+ * as ggml's flash attention does. */
+int orc_dit_forward_masked(const orc_dit * m, const float * input, const float * enc, int N, int T, int enc_S,
+                           float t, float t_r, float * velocity, int n_layers_run, const int * real_S,
+                           const int * real_enc_S);
+
 /* Timestep projection of one embedder (dit-graph.h:81-117): temb[H], tproj[6H]. */
 int orc_dit_timestep(const orc_dit * m, const orc_dit_temb * te, float t, float * temb, float * tproj);
 

@@ -320,6 +320,8 @@ def _models_lib():
         L.orc_qw3lm_decode.argtypes = [C.POINTER(Qwen3), C.POINTER(KV), I, P, P, I, P, I, I]
         L.orc_dit_forward.restype = I
         L.orc_dit_forward.argtypes = [C.POINTER(DiT), P, P, I, I, I, F, F, P, I]
+        L.orc_dit_forward_masked.restype = I
+        L.orc_dit_forward_masked.argtypes = [C.POINTER(DiT), P, P, I, I, I, F, F, P, I, P, P]
         L._models_bound = True
     return L
 
@@ -441,14 +443,19 @@ class OracleDiT:
                      T("proj_in_w"), T("proj_in_b"), T("cond_w"), T("cond_b"), self.layers, T("norm_out"),
                      T("out_ss"), T("proj_out_w"), T("proj_out_b"))
 
-    def forward(self, x, enc, t, t_r, n_layers_run=-1):
+    def forward(self, x, enc, t, t_r, n_layers_run=-1, real_S=None, real_enc_S=None):
+        """real_S / real_enc_S: per-sequence real patch positions / condition rows (padding
+        masks of dit_ggml_generate), or None."""
         x = _f32(x)
         enc = _f32(enc)
         N, T_, _ = x.shape
         enc_S = enc.shape[1]
         out = np.empty((N, T_, self.cfg["out_ch"]), dtype=np.float32)
-        rc = _models_lib().orc_dit_forward(C.byref(self.m), _p(x), _p(enc), N, T_, enc_S, t, t_r, _p(out),
-                                           n_layers_run)
+        rs = None if real_S is None else np.ascontiguousarray(real_S, dtype=np.int32)
+        re = None if real_enc_S is None else np.ascontiguousarray(real_enc_S, dtype=np.int32)
+        rc = _models_lib().orc_dit_forward_masked(C.byref(self.m), _p(x), _p(enc), N, T_, enc_S, t, t_r, _p(out),
+                                                  n_layers_run, None if rs is None else _p(rs),
+                                                  None if re is None else _p(re))
         assert rc == 0
         return out
 
@@ -552,23 +559,46 @@ def dit_from_gguf_tensors(cfg, tensors):
 
 
 def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, momentum=-0.75, norm_threshold=2.5,
-                 solver="euler"):
-    """dit_ggml_generate (src/dit-sampler.h:132-711) over an OracleDiT with the Euler solver or
-    DPM++ 3M (solver="dpm3m", solver-dpm.h:14-50): batched CFG with APG in double when
-    guidance_scale > 1 and a null condition is given. Returns x0 [N][T][out_ch]."""
+                 solver="euler", real_S=None, real_enc_S=None, seeds=None, randn=None, context_switch=None,
+                 cover_steps=-1, enc_switch=None, real_enc_S_switch=None):
+    """dit_ggml_generate (src/dit-sampler.h:132-711) over an OracleDiT with the Euler solver,
+    DPM++ 3M (solver="dpm3m", solver-dpm.h:14-50) or SDE ancestral (solver="sde",
+    solver-sde.h:17-38; randn(seed, n) gives the fresh noise of track b at step k from seed
+    seeds[b] + k + 1): batched CFG with APG in double when guidance_scale > 1 and a null
+    condition is given; padding masks from real_S / real_enc_S (the unconditional slots use
+    their track's lengths, :276-281,300-302); cover mode (:414-449): from step cover_steps on,
+    the context of every slot is context_switch and the conditional slots' condition is
+    enc_switch (with real_enc_S_switch, for the conditional slots only: the unconditional slots
+    keep their cross-attention mask). Returns x0 [N][T][out_ch]."""
     N, T, Oc = noise.shape
     xt = noise.astype(np.float32).copy()
     hist1 = hist2 = None
     cfg_on = guidance_scale > 1.0 and null_emb is not None
     ra = None
+    rs = None if real_S is None else np.asarray(real_S, np.int32)
+    re = None if real_enc_S is None else np.asarray(real_enc_S, np.int32)
+    re_unc = re
+    switched = False
     for step, t in enumerate(schedule):
+        if context_switch is not None and cover_steps >= 0 and step >= cover_steps and not switched:
+            switched = True
+            context = context_switch
+            if enc_switch is not None:
+                enc = enc_switch
+                if real_enc_S_switch is not None:
+                    re = np.asarray(real_enc_S_switch, np.int32)
         x_in = np.concatenate([context, xt], axis=2).astype(np.float32)
+        rs_g, re_g = rs, re
         if cfg_on:
             x_in = np.concatenate([x_in, x_in])
             e = np.concatenate([enc, np.broadcast_to(null_emb, enc.shape)]).astype(np.float32)
+            rs_g = None if rs is None else np.concatenate([rs, rs])
+            if re is not None or re_unc is not None:
+                full = np.full(N, enc.shape[1], np.int32)
+                re_g = np.concatenate([full if re is None else re, full if re_unc is None else re_unc])
         else:
             e = enc
-        v = od.forward(x_in, e, float(t), float(t))
+        v = od.forward(x_in, e, float(t), float(t), real_S=rs_g, real_enc_S=re_g)
         if cfg_on:
             cond, unc = v[:N].astype(np.float64), v[N:].astype(np.float64)
             diff = cond - unc
@@ -586,6 +616,11 @@ def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, mo
             return (xt - v * np.float32(t)).astype(np.float32)
         if solver == "dpm3m":
             xt, hist1, hist2 = dpm3m_step(xt, v, hist1, hist2, t, schedule[step + 1])
+            continue
+        if solver == "sde":
+            fresh = np.stack([np.asarray(randn(int(seeds[b]) + step + 1, T * Oc), np.float32).reshape(T, Oc)
+                              for b in range(N)])
+            xt = sde_step(xt, v, fresh, t, schedule[step + 1])
             continue
         dt = np.float32(np.float32(t) - np.float32(schedule[step + 1]))
         xt = (xt - v * dt).astype(np.float32)

@@ -108,6 +108,102 @@ def test_dit_without_null_condition_runs_without_cfg(cuda, tmp_path):
     dit.close()
 
 
+def test_dit_padding_masks_match_oracle(cuda, tmp_path):
+    """dit_ggml_generate's padding masks (dit-sampler.h:244-304) on ragged tracks: sequence b
+    attends only among its real_S[b] patch positions (inside the window on the sliding layers;
+    padded query rows get a zero attention output) and to its real_enc_S[b] condition rows. One
+    evaluation through set_condition / set_lengths / eval, against the oracle's masked forward."""
+    import torch
+    cfg = DIT_TINY
+    path, keep = _model(tmp_path, cfg, seed=12)
+    dit = acb.DiT(path)
+    od = O.dit_from_gguf_tensors(cfg, keep)
+    rng = np.random.default_rng(13)
+    N, T, enc_S = 3, 80, 24  # S = 40 > window 16
+    real_S, real_enc_S = [40, 29, 7], [24, 13, 1]
+    x = rng.standard_normal((N, T, cfg["in_channels"])).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    xd, ed = torch.from_numpy(x).to(cuda), torch.from_numpy(enc).to(cuda)
+    out = torch.empty((N, T, cfg["out_channels"]), dtype=torch.float32, device=cuda)
+    tt = torch.tensor([0.8, 0.8], dtype=torch.float32, device=cuda)
+    dit.set_condition(ed, T)
+    dit.set_lengths(real_S, real_enc_S)
+    got = dit.eval(xd, tt, out).cpu().numpy()
+    ref = od.forward(x, enc, 0.8, 0.8, real_S=real_S, real_enc_S=real_enc_S)
+    assert np.isfinite(got).all()
+    _check(got, ref, 0.9999, 1e-2, "masked evaluation")
+    # the masks change the result (they are not ignored), and all-real lengths are the unmasked model
+    plain = od.forward(x, enc, 0.8, 0.8)
+    assert cos_sim(ref[1], plain[1]) < 0.999
+    dit.set_lengths([40, 40, 40], [24, 24, 24])
+    _check(dit.eval(xd, tt, out).cpu().numpy(), plain, 0.9999, 1e-2, "all-real lengths")
+    dit.close()
+
+
+def _np_randn(seed, n):
+    """A stand-in noise source for the SDE solver (the reference passes its Philox generator)."""
+    return np.random.default_rng(seed).standard_normal(n).astype(np.float32)
+
+
+def test_dit_generate_ex_matches_oracle(cuda, tmp_path):
+    """acb_dit_generate_ex with dit_ggml_generate's arguments: ragged tracks (real_S, real_enc_S),
+    batched CFG + APG, the SDE solver with per-track seeds, and cover mode (context and condition
+    switched at step 2, the conditional slots' condition lengths with them), against the oracle's
+    generate over the same inputs and noise."""
+    cfg = DIT_TINY
+    path, keep = _model(tmp_path, cfg, seed=14)
+    dit = acb.DiT(path)
+    od = O.dit_from_gguf_tensors(cfg, keep)
+    null = keep["null_condition_emb"][1].astype(np.float32)
+    rng = np.random.default_rng(15)
+    N, T, enc_S, Oc = 2, 80, 24, cfg["out_channels"]
+    noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((N, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    ctx2 = rng.standard_normal((N, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    enc2 = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    sched = acb.turbo_schedule(4)
+    seeds = [1234, 98765]
+    kw = dict(real_S=[40, 31], real_enc_S=[24, 17])
+    for solver in ("euler", "sde", "dpm3m"):
+        x0, ms = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver=solver, seeds=seeds,
+                                 randn=_np_randn, **kw)
+        ref = O.dit_generate(od, noise, ctx, enc, null, sched, 3.0, solver=solver, seeds=seeds, randn=_np_randn, **kw)
+        assert np.isfinite(x0).all() and ms > 0
+        _check(x0, ref, 0.9999, 1e-2, f"generate_ex {solver}")
+    cover = dict(context_switch=ctx2, cover_steps=2, enc_switch=enc2, real_enc_S_switch=[9, 24])
+    x0, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, **kw, **cover)
+    ref = O.dit_generate(od, noise, ctx, enc, null, sched, 3.0, **kw, **cover)
+    _check(x0, ref, 0.9999, 1e-2, "generate_ex cover mode")
+    dit.close()
+
+
+def test_dit_generate_ex_cancel_and_unsupported(cuda, tmp_path):
+    """The cancel callback is polled before every step; a cancelled run returns ACB_ERR_CANCELLED
+    and the model stays usable. STORK4 and DCW are reported as unsupported, nothing runs."""
+    cfg = DIT_TINY
+    path, keep = _model(tmp_path, cfg, seed=16)
+    dit = acb.DiT(path)
+    rng = np.random.default_rng(17)
+    N, T, enc_S, Oc = 1, 40, 8, cfg["out_channels"]
+    noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((N, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    sched = acb.turbo_schedule(8)
+    polls = []
+    with pytest.raises(acb.AcbError) as e:
+        dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, cancel=lambda k: polls.append(k) or k == 3)
+    assert e.value.status == 9 and polls == [0, 1, 2, 3]
+    a, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, cancel=lambda k: False)
+    b, _ = dit.generate(noise, ctx, enc, sched, guidance_scale=3.0)
+    assert np.array_equal(a, b)
+    for kw in (dict(solver="stork4"), dict(dcw_scaler=0.5)):
+        with pytest.raises(acb.AcbError) as e:
+            dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, **kw)
+        assert e.value.status == 2
+    dit.close()
+
+
 def test_dit_config4_width_matches_oracle(cuda, tmp_path):
     """Config 4 layer shapes (hidden 2048, FFN 6144, 16/8 heads, 1500 frames -> 750 tokens with
     the 128 sliding window, 512 condition rows) with 2 layers and 2 sequences."""
