@@ -257,64 +257,155 @@ def dist_env():
     return ws, rank, local
 
 
+def cpu_dit_tensors(cfg, seed):
+    """DiT weights made on the host for the reference arm, with the reference's tensor names and
+    quantize-tool types (Q8_0 linears, F32 norms / biases / tables, BF16 conv projections), without
+    any GPU or this repository's library: Q8_0 blocks are random int8 values in [-127, 127] with
+    one f16 scale (3.3e-4, the scale of N(0, 0.02) rows); vectors N(base, std). The CPU arm's
+    timing does not depend on the values."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(seed)
+    H, F, L = cfg["hidden_size"], cfg["intermediate_size"], cfg["n_layers"]
+    Nh, Nkv, D = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"]
+    in_ch, oc, P, He = cfg["in_channels"], cfg["out_channels"], cfg["patch_size"], cfg["enc_hidden_size"]
+    out = {}
+    d16 = np.frombuffer(np.float16(3.3e-4).tobytes(), np.uint8)
+
+    def mat(name, N, K):
+        raw = np.empty((N, K // 32, 34), np.uint8)
+        raw[:, :, 0:2] = d16
+        raw[:, :, 2:] = rng.integers(-127, 128, size=(N, K // 32, 32), dtype=np.int8).view(np.uint8)
+        out[name] = (O.Q8_0, raw.reshape(N, K // 32 * 34), K, (N, K))
+
+    def vec(name, shape, base=0.0, std=0.02):
+        out[name] = (O.F32, (base + std * rng.standard_normal(shape, dtype=np.float32)).astype(np.float32),
+                     shape[-1], shape)
+
+    def conv_bf16(name, shape):
+        out[name] = (O.BF16, O.f32_to_bf16_bits(0.02 * rng.standard_normal(shape, dtype=np.float32)), shape[-1], shape)
+
+    for te in ("decoder.time_embed", "decoder.time_embed_r"):
+        mat(f"{te}.linear_1.weight", H, 256)
+        vec(f"{te}.linear_1.bias", (H,))
+        mat(f"{te}.linear_2.weight", H, H)
+        vec(f"{te}.linear_2.bias", (H,))
+        mat(f"{te}.time_proj.weight", 6 * H, H)
+        vec(f"{te}.time_proj.bias", (6 * H,))
+    conv_bf16("decoder.proj_in.1.weight", (H, in_ch, P))
+    vec("decoder.proj_in.1.bias", (H,))
+    mat("decoder.condition_embedder.weight", H, He)
+    vec("decoder.condition_embedder.bias", (H,))
+    for i in range(L):
+        p = f"decoder.layers.{i}"
+        for a in ("self_attn", "cross_attn"):
+            mat(f"{p}.{a}.q_proj.weight", Nh * D, H)
+            mat(f"{p}.{a}.k_proj.weight", Nkv * D, H)
+            mat(f"{p}.{a}.v_proj.weight", Nkv * D, H)
+            mat(f"{p}.{a}.o_proj.weight", H, Nh * D)
+            vec(f"{p}.{a}.q_norm.weight", (D,), 1.0, 0.01)
+            vec(f"{p}.{a}.k_norm.weight", (D,), 1.0, 0.01)
+        vec(f"{p}.self_attn_norm.weight", (H,), 1.0, 0.01)
+        vec(f"{p}.cross_attn_norm.weight", (H,), 1.0, 0.01)
+        vec(f"{p}.mlp_norm.weight", (H,), 1.0, 0.01)
+        mat(f"{p}.mlp.gate_proj.weight", F, H)
+        mat(f"{p}.mlp.up_proj.weight", F, H)
+        mat(f"{p}.mlp.down_proj.weight", H, F)
+        vec(f"{p}.scale_shift_table", (1, 6, H), 0.0, 0.05)
+    vec("decoder.norm_out.weight", (H,), 1.0, 0.01)
+    vec("decoder.scale_shift_table", (1, 2, H), 0.0, 0.05)
+    conv_bf16("decoder.proj_out.1.weight", (H, oc, P))
+    vec("decoder.proj_out.1.bias", (oc,))
+    vec("null_condition_emb", (He,), 0.0, 1.0)
+    return out
+
+
+DIT_2B = dict(n_layers=24, hidden_size=2048, intermediate_size=6144, n_heads=16, n_kv_heads=8, head_dim=128,
+              in_channels=192, out_channels=64, patch_size=2, sliding_window=128, rope_theta=1000000.0,
+              rms_norm_eps=1e-6, enc_hidden_size=2048)
+
+
 def run_reference(args):
-    """Reference arm on the headline's metric and config (config 4 DiT steps/s). The reference's
-    ggml-CPU build cannot be compiled here (its ggml submodule is empty), so the oracle port of its
-    DiT arithmetic runs on all host threads. Each timed step is a bounded sample: one evaluation
-    of a CFG pair of sequences (cond + uncond of one track) with one layer; the 0-layer cost is
-    measured once in warm-up, and a full step is (t0 + n_layers * (t1 - t0)) * 4 (every layer and
-    every sequence pair does the same work). Under torchrun only rank 0 runs."""
+    """Reference arm on the headline's metric and config (config 4 DiT denoise steps/s). The
+    reference's ggml-CPU build cannot be compiled here (its ggml submodule is empty), so the CPU
+    oracle -- the port of its DiT arithmetic: Q8_0 x Q8_0-quantised integer block dots, f32
+    attention, rounding per graph node -- runs on all host threads. No GPU and none of this
+    repository's CUDA library is touched: the weights are made on the host (cpu_dit_tensors).
+
+    Work: full-depth evaluations of one CFG pair (2 of the step's 8 sequences of 750 tokens, 512
+    condition rows), run a slice of consecutive layers per timed step so that the run ends in a few
+    minutes; the hidden state carries from slice to slice, and after layer 23 the output
+    projection closes the evaluation and the next begins. Each step's unit is the fraction of a
+    denoise step it did (layers / 24 x 2 / 8 sequences); value = the fractions summed over the K
+    timed steps / their total time. The layer count per slice comes from one warm-up layer
+    (about 5 s per slice). Under torchrun only rank 0 runs."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    import tempfile
-
     import numpy as np
-    import torch
-
-    import synthetic
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    O.set_threads(os.cpu_count() or 1)
-    cfg = dict(synthetic.ACESTEP_DIT_2B)
+    O.set_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
+    cfg = dict(DIT_2B)
     L = cfg["n_layers"]
-    one = dict(cfg, n_layers=1)
-    keep = {}
-    path = os.path.join(tempfile.gettempdir(), "acb_ref_dit_1layer.gguf")
-    synthetic.write_dit_gguf(path, one, synthetic.Q8_0, seed=21, device="cuda" if torch.cuda.is_available() else "cpu",
-                             keep=keep)
-    os.remove(path)
-    od = O.dit_from_gguf_tensors(one, keep)
+    t0 = time.perf_counter()
+    keep = cpu_dit_tensors(cfg, seed=21)
+    od = O.dit_from_gguf_tensors(cfg, keep)
+    t_setup = time.perf_counter() - t0
     rng = np.random.default_rng(1)
     T, enc_S = DIT_T, DIT_ENC_S
-    x = rng.standard_normal((2, T, cfg["in_channels"])).astype(np.float32)
-    e = rng.standard_normal((2, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    x = rng.standard_normal((2, T, cfg["in_channels"]), dtype=np.float32)
+    e = rng.standard_normal((2, enc_S, cfg["enc_hidden_size"]), dtype=np.float32)
+    frac_per_layer = (1.0 / L) * (2.0 / (2 * DIT_TRACKS))
+    state = {"layer": 0, "open": False}
+
+    def slice_(n):
+        """Run the next n layers of the evaluation chain; returns the denoise-step fraction done."""
+        if not state["open"]:
+            od.begin(x, e, 0.75, 0.75)
+            state["open"] = True
+        l0 = state["layer"]
+        l1 = min(L, l0 + n)
+        od.run_layers(l0, l1)
+        state["layer"] = l1
+        if l1 == L:
+            od.finish()
+            state.update(layer=0, open=False)
+        return (l1 - l0) * frac_per_layer
+
+    # warm-up: one layer sets the slice length, then W-1 slices at that length
     t0 = time.perf_counter()
-    od.forward(x, e, 0.5, 0.5, n_layers_run=0)
-    t_base = time.perf_counter() - t0
-    steps = max(1, min(args.steps, 16))
-    samples = []
-    for _ in range(steps):
+    slice_(1)
+    t_layer = time.perf_counter() - t0
+    n_l = int(max(1, min(L, round(5.0 / max(t_layer, 1e-3)))))
+    for _ in range(max(0, args.warmup - 1)):
+        slice_(n_l)
+    fr, dts = [], []
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        od.forward(x, e, 0.5, 0.5, n_layers_run=1)
-        t_one = time.perf_counter() - t0
-        samples.append((t_base + L * max(t_one - t_base, 0.0)) * (2 * DIT_TRACKS // 2))
-    step_s = statistics.median(samples)
-    val = 1.0 / step_s
+        f = slice_(n_l)
+        dts.append(time.perf_counter() - t0)
+        fr.append(f)
+    val = sum(fr) / sum(dts)
+    ms_step = 1e3 * sum(dts) / len(dts)
     cores = O.get_threads()
     line = {"metric": "DiT denoise steps/s (config 4: 24 layers, hidden 2048, Q8_0, 4 tracks x CFG 2 = 8 "
                       "sequences of 750 tokens, 512 condition rows, turbo Euler + APG)",
-            "value": round(val, 6), "unit": "step/s", "impl": "reference", "n_gpus": args.gpus, "steps": steps,
-            "warmup": 1, "ms_per_step": round(step_s * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+            "value": round(val, 6), "unit": "step/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 1), "higher_is_better": True, "scaling": "strong",
             "dtype": "int8 dot products (Q8_0 x Q8_0-quantised activations), f32 elsewhere", "data": "synthetic",
             "config": {"workload": "config4_dit2b_q8_0_turbo_cfg", "tracks": DIT_TRACKS, "sequences": 2 * DIT_TRACKS,
-                       "frames": T, "enc_rows": enc_S},
+                       "frames": T, "enc_rows": enc_S, "layers": L},
             "cpu_baseline": {"value": round(val, 6), "unit": "step/s", "cores": cores, "kind": "port",
-                             "sample": f"per step: oracle evaluation of one CFG pair (2 sequences) through 1 "
-                                       f"layer, 0-layer base {t_base:.1f} s measured once, extrapolated to {L} "
-                                       f"layers x 4 sequence pairs"},
+                             "sample": f"each timed step: {n_l} consecutive layers of a full-depth 24-layer evaluation "
+                                       f"of one CFG pair (2 of 8 sequences), hidden state carried between steps; "
+                                       f"{args.steps} steps = {sum(fr):.4f} denoise steps of work in "
+                                       f"{sum(dts):.1f} s (weights made on the host in {t_setup:.0f} s)"},
             "e2e": {"value": round(val, 6), "unit": "step/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "reference ggml-CPU build unavailable (ggml submodule absent); oracle port timed instead"}
+            "step_fraction": round(fr[0], 6),
+            "note": "reference ggml-CPU build unavailable (ggml submodule absent); the oracle port of its "
+                    "arithmetic is timed instead, on the host cores only"}
     print(json.dumps(line), flush=True)
 
 

@@ -449,75 +449,133 @@ int orc_dit_forward(const orc_dit * m, const float * input, const float * enc_in
     return orc_dit_forward_masked(m, input, enc_in, N, T, enc_S, t, t_r, velocity, n_layers_run, NULL, NULL);
 }
 
-int orc_dit_forward_masked(const orc_dit * m, const float * input, const float * enc_in, int N, int T, int enc_S,
-                           float t, float t_r, float * velocity, int n_layers_run, const int * real_S,
-                           const int * real_enc_S) {
-    const int     H = m->H, P = m->P, S = T / P;
-    const int64_t R  = (int64_t) N * S;
-    int           rc = 0;
+/* One evaluation in three parts, so that a caller can run the layers in slices (the CPU
+ * baseline times real layers of a full-depth evaluation a few at a time). */
+struct orc_dit_state {
+    int       N, T, S, enc_S, rc;
+    int *     real_S;
+    int *     real_enc_S;
+    float *   temb;
+    float *   tproj;
+    float *   hidden;
+    float *   enc;
+    float *   rope;
+};
+
+orc_dit_state * orc_dit_begin(const orc_dit * m, const float * input, const float * enc_in, int N, int T, int enc_S,
+                              float t, float t_r, const int * real_S, const int * real_enc_S) {
+    const int H = m->H, P = m->P;
     if (T % P != 0) {
-        return -1;
+        return NULL;
     }
+    const int       S = T / P;
+    const int64_t   R = (int64_t) N * S;
+    orc_dit_state * st = (orc_dit_state *) calloc(1, sizeof(orc_dit_state));
+    st->N = N, st->T = T, st->S = S, st->enc_S = enc_S;
+    if (real_S) {
+        st->real_S = (int *) malloc(sizeof(int) * N);
+        memcpy(st->real_S, real_S, sizeof(int) * N);
+    }
+    if (real_enc_S) {
+        st->real_enc_S = (int *) malloc(sizeof(int) * N);
+        memcpy(st->real_enc_S, real_enc_S, sizeof(int) * N);
+    }
+    int rc = 0;
     /* timestep embeddings: t and t - t_r, summed (dit-graph.h:537-562) */
-    float * temb   = fbuf(H);
+    st->temb       = fbuf(H);
+    st->tproj      = fbuf(6 * H);
     float * temb_r = fbuf(H);
-    float * tproj  = fbuf(6 * H);
     float * tprojr = fbuf(6 * H);
-    rc |= orc_dit_timestep(m, &m->te, t, temb, tproj);
+    rc |= orc_dit_timestep(m, &m->te, t, st->temb, st->tproj);
     rc |= orc_dit_timestep(m, &m->te_r, t - t_r, temb_r, tprojr);
     for (int i = 0; i < H; i++) {
-        temb[i] = temb[i] + temb_r[i];
+        st->temb[i] = st->temb[i] + temb_r[i];
     }
     for (int i = 0; i < 6 * H; i++) {
-        tproj[i] = tproj[i] + tprojr[i];
+        st->tproj[i] = st->tproj[i] + tprojr[i];
     }
+    free(temb_r);
+    free(tprojr);
 
     /* proj_in on the patchified input: [N][S][in_ch*P] is a reshape of [N][T][in_ch] */
-    float * hidden = fbuf(R * H);
-    rc |= linear(&m->proj_in_w, input, R, hidden);
-    add_bias(hidden, R, H, &m->proj_in_b);
+    st->hidden = fbuf(R * H);
+    rc |= linear(&m->proj_in_w, input, R, st->hidden);
+    add_bias(st->hidden, R, H, &m->proj_in_b);
 
     /* condition embedder */
-    float * enc = fbuf((int64_t) N * enc_S * H);
-    rc |= linear(&m->cond_w, enc_in, (int64_t) N * enc_S, enc);
-    add_bias(enc, (int64_t) N * enc_S, H, &m->cond_b);
+    st->enc = fbuf((int64_t) N * enc_S * H);
+    rc |= linear(&m->cond_w, enc_in, (int64_t) N * enc_S, st->enc);
+    add_bias(st->enc, (int64_t) N * enc_S, H, &m->cond_b);
 
     /* positions 0..S-1 per batch element */
-    int32_t * pos  = (int32_t *) malloc(sizeof(int32_t) * S);
-    float *   rope = fbuf((int64_t) S * m->D);
+    int32_t * pos = (int32_t *) malloc(sizeof(int32_t) * S);
+    st->rope      = fbuf((int64_t) S * m->D);
     for (int i = 0; i < S; i++) {
         pos[i] = i;
     }
-    orc_rope_cache(rope, pos, S, m->D, m->rope_theta);
+    orc_rope_cache(st->rope, pos, S, m->D, m->rope_theta);
+    free(pos);
+    st->rc = rc;
+    return st;
+}
 
-    int nl = n_layers_run < 0 || n_layers_run > m->n_layers ? m->n_layers : n_layers_run;
-    for (int l = 0; l < nl && rc == 0; l++) {
-        rc |= dit_layer(m, &m->layers[l], hidden, enc, N, S, enc_S, tproj, rope, real_S, real_enc_S);
+int orc_dit_run_layers(const orc_dit * m, orc_dit_state * st, int l0, int l1) {
+    if (!st || l0 < 0 || l1 > m->n_layers) {
+        return -1;
     }
+    for (int l = l0; l < l1 && st->rc == 0; l++) {
+        st->rc |= dit_layer(m, &m->layers[l], st->hidden, st->enc, st->N, st->S, st->enc_S, st->tproj, st->rope,
+                            st->real_S, st->real_enc_S);
+    }
+    return st->rc ? -1 : 0;
+}
 
+int orc_dit_finish(const orc_dit * m, orc_dit_state * st, float * velocity) {
+    const int     H = m->H, P = m->P;
+    const int64_t R = (int64_t) st->N * st->S;
+    int           rc = st->rc;
     /* output adaLN + proj_out (dit-graph.h:588-612) */
     const float * oss       = (const float *) m->out_ss.data;
     float *       out_shift = fbuf(H);
     float *       out_scale = fbuf(H);
     for (int i = 0; i < H; i++) {
-        out_shift[i] = oss[i] + temb[i];
-        out_scale[i] = oss[H + i] + temb[i];
+        out_shift[i] = oss[i] + st->temb[i];
+        out_scale[i] = oss[H + i] + st->temb[i];
     }
     float * norm = fbuf(R * H);
-    orc_adaln(hidden, (const float *) m->norm_out.data, m->eps, out_scale, out_shift, 0, norm, 1, R, H);
+    orc_adaln(st->hidden, (const float *) m->norm_out.data, m->eps, out_scale, out_shift, 0, norm, 1, R, H);
     rc |= linear(&m->proj_out_w, norm, R, velocity);
     add_bias(velocity, R, (int64_t) m->out_ch * P, &m->proj_out_b);
-
     free(out_shift);
     free(out_scale);
     free(norm);
-    free(pos);
-    free(rope);
-    free(enc);
-    free(hidden);
-    free(temb);
-    free(temb_r);
-    free(tproj);
-    free(tprojr);
+    return rc ? -1 : 0;
+}
+
+void orc_dit_state_free(orc_dit_state * st) {
+    if (!st) {
+        return;
+    }
+    free(st->real_S);
+    free(st->real_enc_S);
+    free(st->temb);
+    free(st->tproj);
+    free(st->hidden);
+    free(st->enc);
+    free(st->rope);
+    free(st);
+}
+
+int orc_dit_forward_masked(const orc_dit * m, const float * input, const float * enc_in, int N, int T, int enc_S,
+                           float t, float t_r, float * velocity, int n_layers_run, const int * real_S,
+                           const int * real_enc_S) {
+    orc_dit_state * st = orc_dit_begin(m, input, enc_in, N, T, enc_S, t, t_r, real_S, real_enc_S);
+    if (!st) {
+        return -1;
+    }
+    const int nl = n_layers_run < 0 || n_layers_run > m->n_layers ? m->n_layers : n_layers_run;
+    int       rc = orc_dit_run_layers(m, st, 0, nl);
+    rc |= orc_dit_finish(m, st, velocity);
+    orc_dit_state_free(st);
     return rc ? -1 : 0;
 }

@@ -131,6 +131,16 @@ int orc_dit_forward_masked(const orc_dit * m, const float * input, const float *
                            float t, float t_r, float * velocity, int n_layers_run, const int * real_S,
                            const int * real_enc_S);
 
+/* The evaluation of orc_dit_forward_masked in parts: begin (timestep embeddings, proj_in, the
+ * condition embedder), layers [l0, l1) on the carried hidden state, finish (output adaLN and
+ * proj_out). Used to time full-depth evaluations a slice of layers at a time. */
+typedef struct orc_dit_state orc_dit_state;
+orc_dit_state * orc_dit_begin(const orc_dit * m, const float * input, const float * enc, int N, int T, int enc_S,
+                              float t, float t_r, const int * real_S, const int * real_enc_S);
+int             orc_dit_run_layers(const orc_dit * m, orc_dit_state * st, int l0, int l1);
+int             orc_dit_finish(const orc_dit * m, orc_dit_state * st, float * velocity);
+void            orc_dit_state_free(orc_dit_state * st);
+
 /* Timestep projection of one embedder (dit-graph.h:81-117): temb[H], tproj[6H]. */
 int orc_dit_timestep(const orc_dit * m, const orc_dit_temb * te, float t, float * temb, float * tproj);
 

@@ -322,6 +322,14 @@ def _models_lib():
         L.orc_dit_forward.argtypes = [C.POINTER(DiT), P, P, I, I, I, F, F, P, I]
         L.orc_dit_forward_masked.restype = I
         L.orc_dit_forward_masked.argtypes = [C.POINTER(DiT), P, P, I, I, I, F, F, P, I, P, P]
+        L.orc_dit_begin.restype = P
+        L.orc_dit_begin.argtypes = [C.POINTER(DiT), P, P, I, I, I, F, F, P, P]
+        L.orc_dit_run_layers.restype = I
+        L.orc_dit_run_layers.argtypes = [C.POINTER(DiT), P, I, I]
+        L.orc_dit_finish.restype = I
+        L.orc_dit_finish.argtypes = [C.POINTER(DiT), P, P]
+        L.orc_dit_state_free.restype = None
+        L.orc_dit_state_free.argtypes = [P]
         L._models_bound = True
     return L
 
@@ -456,6 +464,25 @@ class OracleDiT:
         rc = _models_lib().orc_dit_forward_masked(C.byref(self.m), _p(x), _p(enc), N, T_, enc_S, t, t_r, _p(out),
                                                   n_layers_run, None if rs is None else _p(rs),
                                                   None if re is None else _p(re))
+        assert rc == 0
+        return out
+
+    def begin(self, x, enc, t, t_r):
+        """Start an evaluation whose layers run in slices (run_layers), then finish()."""
+        self._x, self._e = _f32(x), _f32(enc)
+        self._shape = self._x.shape
+        self._st = _models_lib().orc_dit_begin(C.byref(self.m), _p(self._x), _p(self._e), self._shape[0],
+                                               self._shape[1], self._e.shape[1], t, t_r, None, None)
+        assert self._st
+
+    def run_layers(self, l0, l1):
+        assert _models_lib().orc_dit_run_layers(C.byref(self.m), self._st, l0, l1) == 0
+
+    def finish(self):
+        out = np.empty((self._shape[0], self._shape[1], self.cfg["out_ch"]), dtype=np.float32)
+        rc = _models_lib().orc_dit_finish(C.byref(self.m), self._st, _p(out))
+        _models_lib().orc_dit_state_free(self._st)
+        self._st = None
         assert rc == 0
         return out
 
