@@ -424,7 +424,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
 
     if args.workloads == "lm5":
-        r = run_lm5(dev, rank, ws)
+        r = run_lm5(dev, rank, ws, gen_len=args.lm5_gen)
         if rank == 0:
             print(json.dumps(dict(r, data="synthetic", dtype="int8-dot/f32 (Q8_K-quantised activations)")),
                   flush=True)
@@ -433,6 +433,17 @@ def run_ours(args):
         return
     if args.workloads == "gemv":
         print(json.dumps(run_gemv_shapes(dev)), flush=True)
+        return
+    if args.workloads == "gemm_exact":
+        # profiling target: three launches of the DiT's dominant kernel (exact gate|up), nothing else
+        import torch as _t
+        A = _t.randn(6000, 6144, device=dev).to(_t.float16)
+        B = (_t.randn(12288, 6144, device=dev) * 0.02).to(_t.float16)
+        C = _t.empty(6000, 12288, device=dev, dtype=_t.float32)
+        for _ in range(3):
+            acb.gemm_bf16(A, B, out=C)
+        _t.cuda.synchronize()
+        print(json.dumps({"workload": "gemm_exact gate|up", "launches": 3}), flush=True)
         return
     if args.workloads.startswith("gemm"):
         which = args.workloads.split(":")[1].split("+") if ":" in args.workloads else None
@@ -490,6 +501,10 @@ def run_ours(args):
             # config 5's LM shards one sequence per GPU: run at every N (all ranks take part)
             torch.cuda.empty_cache()
             line["lm5_decode"] = run_lm5(dev, rank, ws)
+        if "dit5" in wl:
+            # config 5's DiT leg (16 sequences, track pairs per GPU): every N
+            torch.cuda.empty_cache()
+            line["dit5"] = run_dit5_job(args, dev, rank, ws, local, stream)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if ws > 1:
@@ -946,7 +961,9 @@ def run_lm5(dev, rank, ws, prompt_len=LM5_PROMPT, gen_len=LM5_GEN, warm_tokens=1
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    torch.cuda.profiler.start()  # profiler range = the timed decode loop (no effect without a profiler)
     toks, _, gpu_ms = m.generate_greedy([int(toks_w[0, -1])], 0, n_timed)
+    torch.cuda.profiler.stop()
     import multi
     ids = torch.from_numpy(np.concatenate([toks_w[0], toks[0]]).astype(np.int64)).to(dev)
     gathered = multi.gather_rows(ids[None], ws)  # the final token-id gather of the sharded job
@@ -1290,6 +1307,7 @@ def run_dit_job(args, dev, rank, ws, local, stream):
                                   "unit": "TFLOP/s",
                                   "frac": round(fl / ws / (step_ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
                                   "traffic": None, "tensor_work_multiplier": 3 if mode == "exact" else 1}}
+    dom = dominant_gemm(dev, n_loc * S, 2 * cfg["intermediate_size"], cfg["hidden_size"], peaks, kind)
     # end to end: the same steps with the timestep row copied in from pinned host memory and the
     # step's result (xt, or x0 at the last step) read back to pinned host memory every step
     h_tts = torch.empty((DIT_STEPS, 3), dtype=torch.float32, pin_memory=True).copy_(tts)
@@ -1313,7 +1331,8 @@ def run_dit_job(args, dev, rank, ws, local, stream):
                                       if ws > 1 else "single",
                        "l2": "weights 9.4 GB and activations > 126 MB L2: every step streams from HBM",
                        "flops_per_step": fl},
-            "roofline": ex["roofline"], "clocks": ex["clocks"],
+            "roofline": dom["roofline"], "step_roofline": ex["roofline"], "dominant_kernel": dom["detail"],
+            "clocks": ex["clocks"],
             "e2e": {"value": round(e2e_k / (e2e_ms * 1e-3), 3), "unit": "step/s", "h2d_bytes_per_step": 12,
                     "d2h_bytes_per_step": N * T * Oc * 4,
                     "path": "acb_dit_eval + acb_dit_apg + acb_dit_euler with per-step pinned host copies"},
@@ -1325,6 +1344,187 @@ def run_dit_job(args, dev, rank, ws, local, stream):
     del keep
     torch.cuda.empty_cache()
     return line
+
+
+# DRAM bytes of one exact-mode gate|up launch (M=6000, N=12288, K'=6144 f16 operands, f32 output),
+# dram__bytes_read.sum + dram__bytes_write.sum from ncu: profiles/gemm_exact_gate_up_ncu.md
+GEMM_EXACT_GATE_UP_DRAM = None
+
+
+def dominant_gemm(dev, M, N, K, peaks, kind):
+    """The dominant kernel of the DiT step (gemm_tc_kernel, 83% of the step: the gate|up shape at
+    this rank's rows), exact mode (f16 hi/lo operands over K' = 3K), f32 output, timed alone with
+    CUDA events on the launching stream over ~150 ms of back-to-back launches. achieved =
+    algorithmic FLOPs 2*M*N*K per launch / the average launch time, against the measured bf16 burst
+    peak (the kernel is timed alone); the tensor pipe does 3x that work."""
+    import torch
+
+    import acb
+    A = torch.randn(M, 3 * K, device=dev).to(torch.float16)
+    B = (torch.randn(N, 3 * K, device=dev) * 0.02).to(torch.float16)
+    C = torch.empty(M, N, device=dev, dtype=torch.float32)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        acb.gemm_bf16(A, B, out=C)
+    e0.record(st)
+    for _ in range(3):
+        acb.gemm_bf16(A, B, out=C)
+    e1.record(st)
+    torch.cuda.synchronize()
+    reps = max(20, int(150.0 / max(e0.elapsed_time(e1) / 3, 1e-3)))
+    e0.record(st)
+    for _ in range(reps):
+        acb.gemm_bf16(A, B, out=C)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / reps * 1e3
+    alg = 2.0 * M * N * K
+    ach = alg / (us * 1e-6) / 1e12
+    traffic = GEMM_EXACT_GATE_UP_DRAM if (M, N, K) == (6000, 12288, 2048) else None
+    del A, B, C
+    return {"roofline": {"kernel": f"gemm_tc_kernel<f16, pair> exact mode, gate|up M={M} N={N} K={K} (K'={3 * K})",
+                         "bound": "tensor", "achieved": round(ach, 1), "peak": peaks["bf16_tflops"],
+                         "peak_kind": kind + " burst", "unit": "TFLOP/s", "frac": round(ach / peaks["bf16_tflops"], 4),
+                         "traffic": traffic, "algorithmic_bytes": int(2 * (M + N) * 3 * K + 4 * M * N),
+                         "tensor_work_multiplier": 3},
+            "detail": {"us_per_launch": round(us, 1), "launches_timed": reps,
+                       "tensor_work_TFLOP/s": round(3 * ach, 1),
+                       "tensor_frac_of_burst": round(3 * ach / peaks["bf16_tflops"], 4)}}
+
+
+DIT5_TRACKS, DIT5_STEPS, DIT5_TIMED = 8, 50, 10
+
+
+def run_dit5_job(args, dev, rank, ws, local, stream):
+    """Config 5's DiT leg: the config-4 DiT on the sft schedule (50 steps, shift 1,
+    pipeline-synth-ops.cpp:289-309) for 8 tracks x CFG 2 = 16 sequences. Every rank owns whole
+    track pairs (track r*8/N .. (r+1)*8/N - 1 with its unconditional twin), so guidance needs no
+    exchange during the steps (one pair per GPU at 8 GPUs); the x0 of every track is gathered over
+    NCCL at the end, outside the timed region. Timed: DIT5_TIMED consecutive steps of the schedule
+    after warm-up steps, CUDA events, max over ranks; value = steps of the whole 16-sequence job per
+    second (strong scaling)."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+    import synthetic
+
+    import multi
+
+    cfg = dict(synthetic.ACESTEP_DIT_2B)
+    N, T, enc_S, Oc = DIT5_TRACKS, DIT_T, DIT_ENC_S, cfg["out_channels"]
+    S, ctx_ch = T // cfg["patch_size"], cfg["in_channels"] - Oc
+    if N % ws:
+        raise SystemExit(f"config 5 DiT: {N} tracks do not shard over {ws} ranks")
+    nt = N // ws
+    mine = list(range(rank * nt, (rank + 1) * nt))
+    slots = mine + [N + t for t in mine]  # local order: conditional tracks, then their twins
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+
+    path = os.path.join(tempfile.gettempdir(), "acb_bench_dit2b_q8_0_c5.gguf")
+    if rank == 0:
+        synthetic.write_dit_gguf(path, cfg, synthetic.Q8_0, seed=21, device=str(dev))
+    barrier()
+    dit = acb.DiT(path, device=local)
+    import gguf
+    null = np.array([t for t in gguf.GGUFReader(path).tensors if t.name == "null_condition_emb"][0].data,
+                    dtype=np.float32).reshape(-1)
+    barrier()
+    if rank == 0:
+        os.remove(path)
+    rng = np.random.default_rng(55)
+    noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((N, T, ctx_ch)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    enc_loc = np.stack([np.broadcast_to(null, enc.shape[1:]) if j >= N else enc[j] for j in slots])
+    dit.set_condition(torch.from_numpy(np.ascontiguousarray(enc_loc)).to(dev), T)
+    tracks = torch.tensor([j % N for j in slots], device=dev)
+    inp = torch.zeros((2 * nt, T, cfg["in_channels"]), device=dev)
+    inp[:, :, :ctx_ch] = torch.from_numpy(ctx).to(dev)[tracks]
+    noise_d = torch.from_numpy(noise[mine]).to(dev)
+    xt = noise_d.clone()
+    vel = torch.empty((2 * nt, T, Oc), device=dev)
+    vt = torch.empty((nt, T, Oc), device=dev)
+    x0 = torch.empty((nt, T, Oc), device=dev)
+    ra = torch.empty((nt, T, Oc), dtype=torch.float64, device=dev)
+    sched = acb.turbo_schedule(DIT5_STEPS, shift=1.0)  # shift 1: t_i = 1 - i/50
+    tts = torch.tensor([[t, t, sched[i + 1] if i + 1 < DIT5_STEPS else 0.0] for i, t in enumerate(sched)],
+                       dtype=torch.float32, device=dev)
+    loc_tr = torch.arange(nt, device=dev).repeat(2)
+
+    def step(k, h_tt=None, h_out=None):
+        i = k % DIT5_STEPS
+        tt = tts[i]
+        if h_tt is not None:
+            tt = h_tt[1]
+            tt.copy_(h_tt[0][i], non_blocking=True)
+        inp[:, :, ctx_ch:] = xt[loc_tr]
+        dit.eval(inp, tt, vel)
+        acb.dit_apg(vel[:nt], vel[nt:], ra, i == 0, DIT_GUIDANCE, vt)
+        last = i == DIT5_STEPS - 1
+        acb.dit_euler(xt, vt, tt, last, out=x0)
+        if last:
+            xt.copy_(noise_d)
+        if h_out is not None:
+            h_out.copy_(x0 if last else xt, non_blocking=True)
+
+    def timed(K, **kw):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(K):
+            step(k, **kw)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return multi.max_over_ranks(e0.elapsed_time(e1), ws, dev)
+
+    for k in range(max(args.warmup, 3)):
+        step(k)
+    K = DIT5_TIMED
+    ms = timed(K)
+    h_tts = torch.empty((DIT5_STEPS, 3), dtype=torch.float32, pin_memory=True).copy_(tts)
+    d_tt = torch.empty(3, dtype=torch.float32, device=dev)
+    h_out = torch.empty((nt, T, Oc), dtype=torch.float32, pin_memory=True)
+    e2e_ms = timed(K, h_tt=(h_tts, d_tt), h_out=h_out)
+    # the whole generate's result: every rank's x0 gathered (NCCL, outside the timed region)
+    for k in range(DIT5_STEPS):
+        step(k)
+    x0_all = multi.gather_rows(x0, ws)
+    peaks, kind = measured_peaks()
+    fl = dit_step_flops(cfg, 2 * N, S, enc_S)
+    step_ms = ms / K
+    ach = fl / (step_ms * 1e-3) / 1e12
+    res = {"metric": "DiT denoise steps/s (config 5 DiT: sft 50 steps, shift 1, 8 tracks x CFG 2 = 16 sequences "
+                     "of 750 tokens)",
+           "value": round(K / (ms * 1e-3), 3), "unit": "step/s", "n_gpus": ws, "steps": K,
+           "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "strong",
+           "config": {"workload": "config5_dit2b_q8_0_sft50_cfg", "tracks": N, "sequences": 2 * N,
+                      "tracks_per_gpu": nt, "frames": T, "enc_rows": enc_S,
+                      "schedule": "sft, shift 1, 50 steps (timed: steps 3..12 of the cycle)",
+                      "parallelism": f"track pairs per GPU ({nt}), no per-step exchange; x0 gathered at the end"
+                                     if ws > 1 else "single", "flops_per_step": fl},
+           "roofline": {"kernel": "whole denoise step (tcgen05 GEMMs dominate)", "bound": "tensor",
+                        "achieved": round(ach / ws, 1), "peak": peaks["bf16_tflops_sustained"],
+                        "peak_kind": kind + " sustained", "unit": "TFLOP/s",
+                        "frac": round(ach / ws / peaks["bf16_tflops_sustained"], 4), "traffic": None,
+                        "tensor_work_multiplier": 3},
+           "e2e": {"value": round(K / (e2e_ms * 1e-3), 3), "unit": "step/s", "h2d_bytes_per_step": 12,
+                   "d2h_bytes_per_step": nt * T * Oc * 4,
+                   "path": "acb_dit_eval + acb_dit_apg + acb_dit_euler with per-step pinned host copies"},
+           "x0_gathered": list(x0_all.shape), "x0_finite": bool(torch.isfinite(x0_all).all().item()),
+           "cpu_baseline": None,
+           "note": "the CPU reference arm times config 4's step; one config-5 step is the same work for 16 sequences"}
+    dit.close()
+    torch.cuda.empty_cache()
+    return res
 
 
 def cpu_dit_sample(cfg, keep, N, T, enc_S):
@@ -1389,10 +1589,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
-    ap.add_argument("--workloads", default="dit,ops,lm,enc,lm5",
+    ap.add_argument("--lm5-gen", type=int, default=LM5_GEN, help="config 5 LM tokens (profiling runs use fewer)")
+    ap.add_argument("--workloads", default="dit,ops,lm,enc,lm5,dit5",
                     help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
                          "decode), enc (config 1 text encoder) -- those three at N=1 as sub-results -- and lm5 "
-                         "(config 5's 4B Q4_K_M LM, one sequence per GPU, at every N); without dit, ops is the "
+                         "(config 5's 4B Q4_K_M LM, one sequence per GPU, at every N), dit5 (config 5's DiT leg, "
+                         "track pairs per GPU, at every N); without dit, ops is the "
                          "headline; or one of gemv / gemm / enc / ditmodes / lm5 alone")
     args = ap.parse_args()
     if args.warmup < 3:

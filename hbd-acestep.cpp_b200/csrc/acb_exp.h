@@ -6,8 +6,8 @@
  * Functions, 1980) with fused multiply-adds, exp(r) for |r| <= ln2/2 by its Taylor polynomial
  * of degree 8 in Horner form (truncation below 0.02 ulp), then the power of two applied in two
  * exact halves so that results down to the subnormal range round once. Every step is an IEEE
- * single-precision operation with one rounding (multiply, fused multiply-add, round-to-integer,
- * exponent-field assembly), so the result depends on nothing but x: a C compiler that keeps
+ * single-precision operation with one rounding (multiply, add, fused multiply-add, exponent-field
+ * assembly), so the result depends on nothing but x: a C compiler that keeps
  * these operations separate (no contraction of the plain multiply) and a CUDA kernel give the
  * same bits. Accuracy: within 2 ulp of exp over the whole float range (checked in the tests
  * against a double-precision exp). NaN propagates, x > 88.72 gives +inf, x < -103.98 gives 0.
@@ -24,20 +24,30 @@
 #    if defined(__CUDA_ARCH__)
 #        define ACB_EXP_FMA(a, b, c) __fmaf_rn((a), (b), (c))
 #        define ACB_EXP_MUL(a, b)    __fmul_rn((a), (b))
-#        define ACB_EXP_RINT(a)      rintf(a)
+#        define ACB_EXP_ADD(a, b)    __fadd_rn((a), (b))
 #    else
 #        include <math.h>
 #        define ACB_EXP_FMA(a, b, c) fmaf((a), (b), (c))
 #        define ACB_EXP_MUL(a, b)    ((a) * (b))
-#        define ACB_EXP_RINT(a)      rintf(a)
+#        define ACB_EXP_ADD(a, b)    ((a) + (b))
 #    endif
 #else
 #    include <math.h>
 #    define ACB_EXP_FN           static inline
 #    define ACB_EXP_FMA(a, b, c) fmaf((a), (b), (c))
 #    define ACB_EXP_MUL(a, b)    ((a) * (b))
-#    define ACB_EXP_RINT(a)      rintf(a)
+#    define ACB_EXP_ADD(a, b)    ((a) + (b))
 #endif
+
+ACB_EXP_FN uint32_t acb_exp_bits(float f) {
+    uint32_t u;
+#if defined(__CUDA_ARCH__)
+    u = __float_as_uint(f);
+#else
+    memcpy(&u, &f, 4);
+#endif
+    return u;
+}
 
 /* 2^e as a float for -126 <= e <= 127 (exponent field assembled directly: exact) */
 ACB_EXP_FN float acb_exp_pow2i(int e) {
@@ -61,9 +71,11 @@ ACB_EXP_FN float acb_expf(float x) {
     if (x < -103.972084f) {
         return 0.0f;
     }
-    /* k = rint(x / ln2); r = x - k ln2 (ln2 = LN2_HI + LN2_LO, LN2_HI with 17 significant bits so
-     * that k * LN2_HI is exact for |k| <= 150) */
-    const float k = ACB_EXP_RINT(ACB_EXP_MUL(x, 1.44269502f));
+    /* k = rint(x / ln2) by the round-to-nearest-even of adding 1.5 * 2^23 (|x / ln2| < 2^22, so
+     * the integer lands in the low mantissa bits: k's float value and its int value come out of
+     * two plain additions, no conversion instruction); r = x - k ln2 (ln2 = LN2_HI + LN2_LO) */
+    const float t = ACB_EXP_ADD(ACB_EXP_MUL(x, 1.44269502f), 12582912.0f);
+    const float k = ACB_EXP_ADD(t, -12582912.0f);
     float       r = ACB_EXP_FMA(k, -0.693145751953125f, x);
     r             = ACB_EXP_FMA(k, -1.42860677e-06f, r);
     /* sum_{n<=8} r^n / n! */
@@ -78,7 +90,7 @@ ACB_EXP_FN float acb_expf(float x) {
     p       = ACB_EXP_FMA(p, r, 1.0f);
     /* p * 2^k, k in [-150, 128]: two factors 2^(k/2) and 2^(k - k/2), each a normal float; the
      * first product is exact, the second rounds once (into the subnormals when it must) */
-    const int ki = (int) k;
+    const int ki = (int) (acb_exp_bits(t) - 0x4B400000u);
     const int k1 = ki / 2;
     return ACB_EXP_MUL(ACB_EXP_MUL(p, acb_exp_pow2i(k1)), acb_exp_pow2i(ki - k1));
 }

@@ -3,12 +3,13 @@
 // over the cache, and the greedy argmax that feeds the next step's embedding gather.
 //
 // Attention reproduces ggml-CPU's qwen3_attn_f32 on an f16 cache (src/qwen3-enc.h:101-112):
-//   s_j = (float)(f16(q) . k_j) * scale                  double accumulation of exact products
+//   s_j = (f16(q) . k_j) * scale    f32, in one fixed order: eight sequential sums of 16
+//                                   dimensions, added as ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7))
 //   p_j = f16( exp(s_j - max) * (float)(1/sum) )         sum of exp in double, exp = acb_expf
 //   o   = (float) sum_j p_j v_j                          double accumulation of exact products
-// Products of two f16 values are exact in float, and their double sum is exact unless the
-// terms span ~24 binades, so every split count and lane order gives the same floats (and the
-// oracle's serial loops give them too). The normalised probabilities are rounded before the PV
+// The score order is the same in every kernel that scores keys (and in the oracle); products of
+// two f16 values are exact in float and their double sum is exact unless the terms span ~24
+// binades, so every split count and lane order gives the same P.V floats. The normalised probabilities are rounded before the PV
 // product, so the step runs in two passes over split chunks of the cache: pass 1 writes scores
 // and per-split maxima, pass 2 normalises and forms per-split partial outputs (double), and
 // the last split CTA of each head adds the partials and rounds once.
@@ -191,15 +192,15 @@ __global__ void __launch_bounds__(128) attn_scores_kernel(const float * __restri
             }
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                double acc = 0.0;
+                float acc = 0.0f;
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    acc += (double) __fmul_rn(kf[e], qv[g][e]);
+                    acc = __fadd_rn(acc, __fmul_rn(kf[e], qv[g][e]));  // the product is exact
                 }
-                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-                const float sv = __fmul_rn((float) acc, scale);
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+                const float sv = __fmul_rn(acc, scale);
                 if (j < j1) {
                     if (sub == 0) {
                         scores[(int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride + j] = sv;
@@ -250,27 +251,62 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
     __shared__ double red[4][G];
     __shared__ float  sM[G], sInv[G];
 
-    // global max and sum of expf(s - max) over the whole row, in a fixed order
+    // global max and double sum of exp(s - max) over the whole row; every loop keeps a batch of
+    // loads in flight (a chain of dependent L2 round trips would dominate the kernel)
     float M[G];
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        const float * sm = smax + ((int64_t) t * Nh + hk * G + g) * n_split;
-        float         m  = -INFINITY;
-        for (int i = 0; i < n_split; i++) {
-            m = fmaxf(m, sm[i]);
+        M[g] = -INFINITY;
+    }
+    for (int i0 = 0; i0 < n_split; i0 += 8) {
+        float v[G][8];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float * sm = smax + ((int64_t) t * Nh + hk * G + g) * n_split;
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                v[g][u] = sm[min(i0 + u, n_split - 1)];  // clamped: a repeated maximum changes nothing
+            }
         }
-        M[g] = m;
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                M[g] = fmaxf(M[g], v[g][u]);
+            }
+        }
+    }
+    double ssum[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        ssum[g] = 0.0;
+    }
+    constexpr int US = 8;
+    for (int j0 = threadIdx.x; j0 < kv_len; j0 += 128 * US) {
+        float v[G][US];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const float * sr = scores + (int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride;
+#pragma unroll
+            for (int u = 0; u < US; u++) {
+                v[g][u] = sr[min(j0 + 128 * u, kv_len - 1)];  // clamped: added only if in range
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+#pragma unroll
+            for (int u = 0; u < US; u++) {
+                if (j0 + 128 * u < kv_len) {
+                    ssum[g] += (double) acb_expf(__fsub_rn(v[g][u], M[g]));
+                }
+            }
+        }
     }
 #pragma unroll
     for (int g = 0; g < G; g++) {
-        const float * sr = scores + (int64_t) t * Nh * s_stride + (int64_t) (hk * G + g) * s_stride;
-        double        s  = 0.0;
-        for (int j = threadIdx.x; j < kv_len; j += 128) {
-            s += (double) acb_expf(__fsub_rn(sr[j], M[g]));
-        }
-        s = warp_sum(s);
+        const double sg = warp_sum(ssum[g]);
         if (lane == 0) {
-            red[warp][g] = s;
+            red[warp][g] = sg;
         }
     }
     __syncthreads();
@@ -282,7 +318,9 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
     }
     __syncthreads();
 
-    // partial output over this chunk: lane owns 4 of the D elements, warps split the keys
+    // partial output over this chunk: lane owns 4 of the D elements, warps take blocks of 32 keys.
+    // The probabilities of a block are computed once (lane l: key jb + l, every q head of the
+    // group) and handed to the other lanes by shuffles.
     double acc[G][4];
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -293,35 +331,38 @@ __global__ void __launch_bounds__(128) attn_pv_kernel(const float * __restrict__
     }
     const uint16_t * vb = kv.v + kv_index(kv, Nkv, D, set, hk, 0);
     const float *    sb = scores + (int64_t) t * Nh * s_stride + (int64_t) (hk * G) * s_stride;
-    constexpr int    U  = 4;  // keys in flight per warp
-    for (int jb = j0 + warp; jb < j1; jb += 4 * U) {
-        uint2 raw[U];
-        float sv[U][G];
+    constexpr int    U  = 8;  // V rows in flight per lane
+    for (int jb = j0 + 32 * warp; jb < j1; jb += 32 * 4) {
+        const int n  = min(32, j1 - jb);
+        const int jl = min(jb + lane, j1 - 1);  // clamped: lanes past the chunk carry p = 0
+        float     pl[G];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int j = jb + 4 * u;
-            if (j < j1) {
-                raw[u] = *reinterpret_cast<const uint2 *>(vb + (int64_t) j * D + lane * 4);
-#pragma unroll
-                for (int g = 0; g < G; g++) {
-                    sv[u][g] = sb[(int64_t) g * s_stride + j];
-                }
-            }
+        for (int g = 0; g < G; g++) {
+            const float pe = __fmul_rn(acb_expf(__fsub_rn(sb[(int64_t) g * s_stride + jl], sM[g])), sInv[g]);
+            pl[g]          = lane < n ? __half2float(__float2half_rn(pe)) : 0.0f;
         }
+        for (int u0 = 0; u0 < n; u0 += U) {
+            uint2 raw[U];
 #pragma unroll
-        for (int u = 0; u < U; u++) {
-            const int j = jb + 4 * u;
-            if (j < j1) {
-                const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].x));
-                const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].y));
+            for (int u = 0; u < U; u++) {
+                const int j = jb + min(u0 + u, n - 1);  // clamped: used only below n
+                raw[u]      = *reinterpret_cast<const uint2 *>(vb + (int64_t) j * D + lane * 4);
+            }
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    const float pe = __fmul_rn(acb_expf(__fsub_rn(sv[u][g], sM[g])), sInv[g]);
-                    const float pp = __half2float(__float2half_rn(pe));
-                    acc[g][0] += (double) __fmul_rn(f01.x, pp);
-                    acc[g][1] += (double) __fmul_rn(f01.y, pp);
-                    acc[g][2] += (double) __fmul_rn(f23.x, pp);
-                    acc[g][3] += (double) __fmul_rn(f23.y, pp);
+            for (int u = 0; u < U; u++) {
+                if (u0 + u < n) {  // uniform over the warp
+                    const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].x));
+                    const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&raw[u].y));
+                    const double v0 = f01.x, v1 = f01.y, v2 = f23.x, v3 = f23.y;  // shared by the G heads
+#pragma unroll
+                    for (int g = 0; g < G; g++) {
+                        const double pp = (double) __shfl_sync(0xffffffffu, pl[g], u0 + u);
+                        // p * v is exact (two f16 values): the fused multiply-add rounds only the sum
+                        acc[g][0] = fma(pp, v0, acc[g][0]);
+                        acc[g][1] = fma(pp, v1, acc[g][1]);
+                        acc[g][2] = fma(pp, v2, acc[g][2]);
+                        acc[g][3] = fma(pp, v3, acc[g][3]);
+                    }
                 }
             }
         }

@@ -492,24 +492,41 @@ __device__ __forceinline__ void pd_act_quant(const PdParams & P, PdCtx & x, cons
 // EPI_GATE keeps the rows in shared memory; EPI_UP writes silu(gate) * up of the same rows
 enum { EPI_STORE = 0, EPI_ADD = 1, EPI_HEAD = 2, EPI_GATE = 3, EPI_UP = 4 };
 
-// One 16-row x 32-column tile block for one activation column. Lane 4g + q holds bytes
-// 4q..4q+3 and 16+4q..16+4q+3 of rows g and g + 8 (the tile order) and the activation words q
-// and 4 + q (xw); two dp4a per row give its integer partial sum over those 8 columns. The four
-// lanes of a row add their integer sums exactly (shuffles), and one lane turns the block's sum
-// into its float term (float)isum * (d_w * d_x), added in double to the lane's partials.
-__device__ __forceinline__ void pd_block(const uint4 & a, uint32_t dw, uint2 xw, float dx, double & acc0,
-                                         double & acc2, bool lead) {
-    int s0 = __dp4a((int) a.z, (int) xw.y, __dp4a((int) a.x, (int) xw.x, 0));
-    int s1 = __dp4a((int) a.w, (int) xw.y, __dp4a((int) a.y, (int) xw.x, 0));
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-    const float dl = f16_bits_to_f((uint16_t) (dw & 0xffff));
-    const float dh = f16_bits_to_f((uint16_t) (dw >> 16));
-    if (lead) {
-        acc0 += (double) __fmul_rn((float) s0, __fmul_rn(dl, dx));
-        acc2 += (double) __fmul_rn((float) s1, __fmul_rn(dh, dx));
+// Integer partial sums of one 16-row x 32-column tile block for one activation column. Lane
+// 4g + q holds bytes 4q..4q+3 and 16+4q..16+4q+3 of rows g and g + 8 (the tile order) and the
+// activation words q and 4 + q (xw); two dp4a per row give its partial sum over those 8 columns.
+__device__ __forceinline__ void pd_isum(const uint4 & a, uint2 xw, int & s0, int & s1) {
+    s0 = __dp4a((int) a.z, (int) xw.y, __dp4a((int) a.x, (int) xw.x, 0));
+    s1 = __dp4a((int) a.w, (int) xw.y, __dp4a((int) a.y, (int) xw.x, 0));
+}
+
+// Four blocks' partial sums of one row over the 4 lanes q of the row -> lane q holds the whole
+// integer sum of block q (a transposing butterfly: 3 shuffles instead of 4 x 2).
+__device__ __forceinline__ int pd_transpose4(int v0, int v1, int v2, int v3, int q) {
+    const bool hi2 = q & 2, hi1 = q & 1;
+    int        x0  = hi2 ? v2 : v0;
+    int        x1  = hi2 ? v3 : v1;
+    x0 += __shfl_xor_sync(0xffffffffu, hi2 ? v0 : v2, 2);
+    x1 += __shfl_xor_sync(0xffffffffu, hi2 ? v1 : v3, 2);
+    int z = hi1 ? x1 : x0;
+    z += __shfl_xor_sync(0xffffffffu, hi1 ? x0 : x1, 1);
+    return z;
+}
+
+// Blocks u0..u0+3 of a warp's stage share: lane q turns block u0 + q's integer sums (rows g,
+// g + 8) into their float terms (float)isum * (d_w * d_x) and adds them in double. Sums of
+// blocks that are not there are zero (their terms add 0).
+__device__ __forceinline__ void pd_quad(const int s0[4], const int s1[4], const uint32_t dw[4], const float dx[4],
+                                        int q, double & acc0, double & acc2, bool use) {
+    const int      t0 = pd_transpose4(s0[0], s0[1], s0[2], s0[3], q);
+    const int      t1 = pd_transpose4(s1[0], s1[1], s1[2], s1[3], q);
+    const uint32_t w  = q == 0 ? dw[0] : (q == 1 ? dw[1] : (q == 2 ? dw[2] : dw[3]));
+    const float    d  = q == 0 ? dx[0] : (q == 1 ? dx[1] : (q == 2 ? dx[2] : dx[3]));
+    const float    dl = f16_bits_to_f((uint16_t) (w & 0xffff));
+    const float    dh = f16_bits_to_f((uint16_t) (w >> 16));
+    if (use) {
+        acc0 += (double) __fmul_rn((float) t0, __fmul_rn(dl, d));
+        acc2 += (double) __fmul_rn((float) t1, __fmul_rn(dh, d));
     }
 }
 
@@ -543,7 +560,7 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
     for (int64_t tg = t0; tg < t1; tg += kPdWarps) {
         const int nt = (int) min((int64_t) kPdWarps, t1 - tg);
         for (int j = 0; j < nt; j++) {
-        double acc0 = 0.0, acc2 = 0.0;  // rows g and g + 8: block terms (added by lane q == 0)
+        double acc0 = 0.0, acc2 = 0.0;  // rows g and g + 8: this lane's share of the block terms
         for (int b0 = 0; b0 < nb; b0 += bs) {
             const int       s    = (int) (x.it % (uint32_t) P.slots);
             const bool      have = pd_wait_full(P, x, s, (x.it / (uint32_t) P.slots) & 1);
@@ -551,8 +568,8 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
             // warp w takes nbw consecutive blocks of the stage; every shared-memory operand of
             // its blocks is loaded first. Lane 4g + q holds bytes 4q..4q+3 and 16+4q..16+4q+3 of
             // rows g and g + 8 (the tile order); its two dp4a pairs give those rows' partial sums
-            // over its 8 columns, the 4 lanes of a row add them exactly, and lane q == 0 adds the
-            // block's float term to its double partials.
+            // over its 8 columns; per four blocks the 4 lanes of a row exchange them so that each
+            // lane holds one block's whole integer sum and adds that block's float term.
             const int nbw = (bs + kPdWarps - 1) / kPdWarps, bw0 = warp * nbw;
             if (nbw == kPdBpw && bw0 + kPdBpw <= bs && (b0 & 3) == 0) {
                 // all of this warp's blocks are in the stage: constant offsets (the f16 scales of
@@ -581,21 +598,37 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
                 }
                 // the shuffles inside run on every lane; the terms are added only with the stage
 #pragma unroll
-                for (int u = 0; u < kPdBpw; u++) {
-                    pd_block(a[u], dw[u], xw[u], dx[u], acc0, acc2, have && q == 0);
+                for (int u0 = 0; u0 < kPdBpw; u0 += 4) {
+                    int s0[4], s1[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        pd_isum(a[u0 + u], xw[u0 + u], s0[u], s1[u]);
+                    }
+                    pd_quad(s0, s1, dw + u0, dx + u0, q, acc0, acc2, have);
                 }
             } else {
                 // ragged stage: indices past it are clamped to its last block (loads stay
-                // unconditional: a predicated load sequence costs registers) and skipped
+                // unconditional: a predicated load sequence costs registers) and their sums zeroed
 #pragma unroll
-                for (int u = 0; u < kPdBpw; u++) {
-                    const int   bl = min(bw0 + u, bs - 1);
-                    const int   b  = b0 + bl;
-                    const uint4 a  = *reinterpret_cast<const uint4 *>(st + bl * kPdTileBlk + lane * 16);
-                    const uint32_t dw = *reinterpret_cast<const uint32_t *>(st + bl * kPdTileBlk + 512 + g * 4);
-                    const uint2 xw = *reinterpret_cast<const uint2 *>(xq4 + 8 * b + 2 * q);
-                    const float dx = __half2float(sm_xd()[b]);
-                    pd_block(a, dw, xw, dx, acc0, acc2, have && q == 0 && u < nbw && bw0 + u < bs);
+                for (int u0 = 0; u0 < kPdBpw; u0 += 4) {
+                    int      s0[4], s1[4];
+                    uint32_t dw[4];
+                    float    dx[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int   bl = min(bw0 + u0 + u, bs - 1);
+                        const int   b  = b0 + bl;
+                        const uint4 a  = *reinterpret_cast<const uint4 *>(st + bl * kPdTileBlk + lane * 16);
+                        dw[u]          = *reinterpret_cast<const uint32_t *>(st + bl * kPdTileBlk + 512 + g * 4);
+                        const uint2 xw = *reinterpret_cast<const uint2 *>(xq4 + 8 * b + 2 * q);
+                        dx[u]          = __half2float(sm_xd()[b]);
+                        pd_isum(a, xw, s0[u], s1[u]);
+                        if (!(u0 + u < nbw && bw0 + u0 + u < bs)) {
+                            s0[u] = 0;
+                            s1[u] = 0;
+                        }
+                    }
+                    pd_quad(s0, s1, dw, dx, q, acc0, acc2, have);
                 }
             }
             __syncwarp();
@@ -604,6 +637,10 @@ __device__ __forceinline__ bool pd_gemv(const PdParams & P, PdCtx & x, int64_t n
             }
             x.it++;
         }
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc2 += __shfl_xor_sync(0xffffffffu, acc2, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc2 += __shfl_xor_sync(0xffffffffu, acc2, 2);
         if (q == 0) {
             double * tr = sm_tredd() + (j * kPdWarps + warp) * 16;
             tr[g]       = acc0;
@@ -815,15 +852,17 @@ __device__ void pd_attn_scores(const PdParams & P, PdCtx & x, const acb_decode_l
             }
 #pragma unroll
             for (int g = 0; g < G; g++) {
-                double acc = 0.0;  // products of f16 values are exact in float
+                // the score order of attn_scores_kernel: 16 dimensions per lane in sequence, then
+                // the xor-1/2/4 tree over the key's 8 lanes (products of f16 values are exact)
+                float acc = 0.0f;
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    acc += (double) __fmul_rn(kf[e], qv[g][e]);
+                    acc = __fadd_rn(acc, __fmul_rn(kf[e], qv[g][e]));
                 }
-                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-                acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-                const float sv = __fmul_rn((float) acc, S.attn_scale);
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+                const float sv = __fmul_rn(acc, S.attn_scale);
                 if (j < j1) {
                     if (sub == 0) {
                         P.scores[(int64_t) (h * G + g) * S.max_seq + j] = sv;
@@ -880,15 +919,17 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
     // Its first UV keys (V rows and scores) are requested now: they do not depend on the max.
     const int     g  = warp / WPH, wi = warp % WPH, hq = h * G + g;
     const float * sr = P.scores + (int64_t) hq * S.max_seq;
+    // lane l < UV also loads the score of key u = l of the batch: the batch's probabilities are
+    // computed once (one per lane) and handed to the other lanes by shuffles
     uint2         vr[UV];
-    float         sv[UV];
+    float         sv;
     auto          load_pv = [&](int jb) {
 #pragma unroll
         for (int u = 0; u < UV; u++) {
             const int j = max(j0, min(jb + WPH * u, j1 - 1));  // clamped: used only if in range
             vr[u]       = __ldcg(reinterpret_cast<const uint2 *>(vb + (int64_t) j * kPdD + lane * 4));
-            sv[u]       = __ldcg(sr + j);
         }
+        sv = __ldcg(sr + max(j0, min(jb + WPH * (lane % UV), j1 - 1)));
     };
     int jb = j0 + wi;
     load_pv(jb);
@@ -952,17 +993,19 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
     const float Mg = M[g], ig = sm_misc()[g];
     double4     acc = make_double4(0.0, 0.0, 0.0, 0.0);
     for (;;) {
+        const float pl = f16r(__fmul_rn(acb_expf(__fsub_rn(sv, Mg)), ig));  // key jb + WPH * (lane % UV)
 #pragma unroll
         for (int u = 0; u < UV; u++) {
-            const int j = jb + WPH * u;
+            const int    j  = jb + WPH * u;
+            const double pp = (double) __shfl_sync(0xffffffffu, pl, u);  // every lane takes part
             if (j < j1) {
-                const float  pp  = f16r(__fmul_rn(acb_expf(__fsub_rn(sv[u], Mg)), ig));
                 const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[u].x));
                 const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&vr[u].y));
-                acc.x += (double) __fmul_rn(f01.x, pp);
-                acc.y += (double) __fmul_rn(f01.y, pp);
-                acc.z += (double) __fmul_rn(f23.x, pp);
-                acc.w += (double) __fmul_rn(f23.y, pp);
+                // p * v is exact (two f16 values): the fused multiply-add rounds only the sum
+                acc.x = fma(pp, (double) f01.x, acc.x);
+                acc.y = fma(pp, (double) f01.y, acc.y);
+                acc.z = fma(pp, (double) f23.x, acc.z);
+                acc.w = fma(pp, (double) f23.y, acc.w);
             }
         }
         jb += WPH * UV;
@@ -1006,19 +1049,19 @@ __device__ void pd_attn_pv(const PdParams & P, PdCtx & x, const acb_decode_layer
     const int     s0   = q * ns / Q, s1 = (q + 1) * ns / Q;
     const int64_t off  = (int64_t) (h * G) * kPdD + gl * 4;
     double4       a    = make_double4(0.0, 0.0, 0.0, 0.0);
+    {
+        // every partial of the range requested at once (one L2 round trip on the critical path)
+        double2 v[QMAX][2];
 #pragma unroll
-    for (int i0 = 0; i0 < QMAX; i0 += 4) {
-        double2 v[4][2];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int       si = min(s0 + i0 + i, ns - 1);  // clamped: added only if in the range
+        for (int i = 0; i < QMAX; i++) {
+            const int       si  = min(s0 + i, ns - 1);  // clamped: added only if in the range
             const double2 * src = reinterpret_cast<const double2 *>(P.part + (int64_t) si * Nh * kPdD + off);
             v[i][0]             = __ldcg(src);
             v[i][1]             = __ldcg(src + 1);
         }
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            if (i0 + i < QMAX && s0 + i0 + i < s1) {
+        for (int i = 0; i < QMAX; i++) {
+            if (s0 + i < s1) {
                 a.x += v[i][0].x;
                 a.y += v[i][0].y;
                 a.z += v[i][1].x;

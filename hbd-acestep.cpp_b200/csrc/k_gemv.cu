@@ -581,7 +581,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const GemvParams p) {
 #pragma unroll
             for (int m = 0; m < MT; m++) {
                 if (m < p.M) {
-                    const float v = (float) warp_sum(acc[m]);
+                    // lanes that hold terms: every lane (Q8_0), lanes 0/8/16/24 (Q4_K: one per
+                    // superblock slot), lanes 0/16 (Q6_K); the others hold zero
+                    double t = acc[m];
+                    if (QT == ACB_TYPE_Q8_0) {
+                        t = warp_sum(t);
+                    } else {
+                        if (QT == ACB_TYPE_Q4_K) {
+                            t += __shfl_xor_sync(0xffffffffu, t, 8);
+                        }
+                        t += __shfl_xor_sync(0xffffffffu, t, 16);
+                    }
+                    const float v = (float) t;
                     if (lane == 0) {
                         const int64_t n  = r + rr;
                         float *       yp = p.y + (int64_t) m * p.y_stride + n;

@@ -440,7 +440,8 @@ ACB_API int acb_attn_decode_splits(int n_tok, int Nkv);
 
 /* One-token attention for n_tok sequences over the f16 cache, kv_len = pos[t] + 1, with
  * ggml-CPU semantics (q and normalised probabilities rounded to f16, softmax sum in double):
- *   s_j = (float)(sum_d q16_d k16_jd) * scale, sum in double (every product exact in float)
+ *   s_j = (sum_d q16_d k16_jd) * scale in float, in one fixed order: eight sequential sums of 16
+ *         dimensions added as ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)) (products of f16 are exact)
  *   p_j = f16( acb_expf(s_j - max) * (float)(1 / sum_j acb_expf(s_j - max)) )
  *   o_d = (float) sum_j p_j v16_jd, sum in double
  * so the result is the same for any split count. Scratch (device, caller-owned): scores

@@ -908,18 +908,36 @@ void orc_attention(const float * q, int64_t q_tok_stride, const void * k, const 
                 float x = q[i * q_tok_stride + (int64_t) h * D + d];
                 qv[d]   = f16 ? orc_f16_to_f32(orc_f32_to_f16(x)) : x;
             }
-            /* scores = K . q, then soft_max_ext: x*scale + mask. Dot products and the P.V sums
-             * accumulate in double and round once (on the f16 cache every product is exact in
-             * float, so the sum is exact in any order unless its terms span ~24 binades); the
-             * exponential is acb_expf. */
+            /* scores = K . q, then soft_max_ext: x*scale + mask. On the f16 cache the dot is
+             * summed in float in one fixed order (every product of two f16 values is exact):
+             * eight sequential sums over 16 dimensions each, added as
+             * ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)) -- the order of the decode kernels. The f32
+             * path sums in double. The P.V sums accumulate in double and round once (on the f16
+             * cache every product is exact, so the sum is exact in any order unless its terms
+             * span ~24 binades); the exponential is acb_expf. */
             float mx = -INFINITY;
             for (int64_t j = 0; j < Skv; j++) {
-                double acc = 0.0;
-                for (int d = 0; d < D; d++) {
-                    float kk = kv_at(k, kv_type, j * kv_tok_stride + (int64_t) hk * kv_head_stride + d);
-                    acc += f16 ? (double) (kk * qv[d]) : (double) kk * (double) qv[d];
+                float sv;
+                if (f16 && D == 128) {
+                    float part[8];
+                    for (int c = 0; c < 8; c++) {
+                        float acc = 0.0f;
+                        for (int d = 16 * c; d < 16 * c + 16; d++) {
+                            float kk = kv_at(k, kv_type, j * kv_tok_stride + (int64_t) hk * kv_head_stride + d);
+                            acc      = acc + kk * qv[d];
+                        }
+                        part[c] = acc;
+                    }
+                    sv = (((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]))) *
+                         scale;
+                } else {
+                    double acc = 0.0;
+                    for (int d = 0; d < D; d++) {
+                        float kk = kv_at(k, kv_type, j * kv_tok_stride + (int64_t) hk * kv_head_stride + d);
+                        acc += f16 ? (double) (kk * qv[d]) : (double) kk * (double) qv[d];
+                    }
+                    sv = (float) acc * scale;
                 }
-                float sv = (float) acc * scale;
                 if (mask) {
                     sv = sv + mask[i * Skv + j];
                 }
