@@ -1191,13 +1191,26 @@ def run_dit(dev, rank, want_cpu=True, reps=2, modes=("exact", "fast")):
     return res
 
 
+def make_comm(ws, rank, local):
+    """The library's NCCL communicator (acb_comm) for the sharded DiT job: rank 0 makes the unique
+    id, torch.distributed hands it to the other ranks."""
+    import torch
+
+    import acb
+    if ws == 1:
+        return None
+    obj = [acb.Comm.unique_id() if rank == 0 else None]
+    torch.distributed.broadcast_object_list(obj, src=0)
+    return acb.Comm(obj[0], world=ws, rank=rank, device=local, timeout_ms=120000)
+
+
 def run_dit_job(args, dev, rank, ws, local, stream):
-    """The headline: config 4 denoise steps/s for the whole 8-sequence job (4 tracks x CFG 2), the
-    sequences sharded over the ranks (strong scaling). Each step: every rank evaluates its own
-    sequences (acb_dit_eval, one CUDA graph); an NCCL all-gather assembles the velocities; every
-    rank runs APG + the Euler update for all tracks (identical on every rank). A step of the
-    turbo schedule is one timed unit; after the 8th step the next generation starts from the
-    noise again."""
+    """The headline: config 4 denoise steps/s for the whole 8-sequence job (4 tracks x CFG 2),
+    sharded over the ranks by the library itself (acb_dit_job_* over acb_comm, the C ABI a C++ host
+    uses): whole track pairs per rank at 1, 2 and 4 GPUs (no exchange during the steps), one CFG
+    half per rank at 8 GPUs (the partner ranks swap the step's velocity over NCCL). A step of the
+    turbo schedule is one timed unit; the 8-step schedule is cycled (APG restarts with every
+    cycle). Time: CUDA events on the model's stream, max over ranks."""
     import tempfile
 
     import numpy as np
@@ -1211,12 +1224,8 @@ def run_dit_job(args, dev, rank, ws, local, stream):
     cfg = dict(synthetic.ACESTEP_DIT_2B)
     N, T, enc_S, Oc = DIT_TRACKS, DIT_T, DIT_ENC_S, cfg["out_channels"]
     Ng, S, ctx_ch = 2 * N, T // cfg["patch_size"], cfg["in_channels"] - Oc
-    try:
-        slots = multi.dit_slots(Ng, ws, rank)
-    except ValueError as e:
-        raise SystemExit(f"config 4: {e}")
-    n_loc = len(slots)
-    slot_track, slot_uncond = multi.slot_tracks(slots, N)
+    t0_, n_loc_tr, half, _ = acb.dit_shard_plan(N, 1, ws, rank)
+    n_loc = 1 if half >= 0 else 2 * n_loc_tr  # sequences this rank evaluates
 
     def barrier():
         if ws > 1:
@@ -1229,57 +1238,40 @@ def run_dit_job(args, dev, rank, ws, local, stream):
         synthetic.write_dit_gguf(path, cfg, synthetic.Q8_0, seed=21, device=str(dev), keep=keep)
     barrier()
     dit = acb.DiT(path, device=local)
-    import gguf
-    null = np.array([t for t in gguf.GGUFReader(path).tensors if t.name == "null_condition_emb"][0].data,
-                    dtype=np.float32).reshape(-1)
     barrier()
     if rank == 0:
         os.remove(path)
+    comm = make_comm(ws, rank, local)
 
     rng = np.random.default_rng(17)
     noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
     ctx = rng.standard_normal((N, T, ctx_ch)).astype(np.float32)
     enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
-    enc_loc = np.stack([np.broadcast_to(null, enc.shape[1:]) if u else enc[tr] for tr, u in zip(slot_track, slot_uncond)])
-    dit.set_condition(torch.from_numpy(np.ascontiguousarray(enc_loc)).to(dev), T)
-    tracks = torch.tensor(slot_track, device=dev)
-    inp = torch.zeros((n_loc, T, cfg["in_channels"]), device=dev)
-    inp[:, :, :ctx_ch] = torch.from_numpy(ctx).to(dev)[tracks]
-    noise_d = torch.from_numpy(noise).to(dev)
-    xt = noise_d.clone()
-    vel_loc = torch.empty((n_loc, T, Oc), device=dev)
-    vt = torch.empty((N, T, Oc), device=dev)
-    x0 = torch.empty((N, T, Oc), device=dev)
-    ra = torch.empty((N, T, Oc), dtype=torch.float64, device=dev)
     sched = acb.turbo_schedule(DIT_STEPS)
-    tts = torch.tensor([[t, t, sched[i + 1] if i + 1 < DIT_STEPS else 0.0] for i, t in enumerate(sched)],
-                       dtype=torch.float32, device=dev)
+    L = acb.lib()
+    C = __import__("ctypes")
+    ms_stream = torch.cuda.ExternalStream(L.acb_dit_stream(dit.h), device=dev)
 
-    def step(k, h_tt=None, h_out=None):
+    def job_begin():
+        acb._check("acb_dit_job_begin", L.acb_dit_job_begin(
+            dit.h, comm.h if comm else None, noise.ctypes.data, ctx.ctypes.data, enc.ctypes.data, enc_S, T, N,
+            float(DIT_GUIDANCE), None, -1, None, None, None, None, None, None, None, b"euler", None, None))
+
+    def step(k, h_out=None):
         i = k % DIT_STEPS
-        tt = tts[i]
-        if h_tt is not None:  # end-to-end: this step's timestep row from pinned host memory
-            tt = h_tt[1]
-            tt.copy_(h_tt[0][i], non_blocking=True)
-        inp[:, :, ctx_ch:] = xt[tracks]
-        dit.eval(inp, tt, vel_loc)
-        vel_all = multi.gather_rows(vel_loc, ws)  # slot order: conditional tracks, then their twins
-        acb.dit_apg(vel_all[:N], vel_all[N:], ra, i == 0, DIT_GUIDANCE, vt)
         last = i == DIT_STEPS - 1
-        acb.dit_euler(xt, vt, tt, last, out=x0)
-        if last:
-            xt.copy_(noise_d)
-        if h_out is not None:  # end-to-end: the step's result back to pinned host memory
-            h_out.copy_(x0 if last else xt, non_blocking=True)
+        acb._check("acb_dit_job_step", L.acb_dit_job_step(
+            dit.h, i, float(sched[i]), float(sched[i + 1]) if not last else 0.0, int(last),
+            C.c_void_p(h_out.data_ptr()) if h_out is not None else None))
 
     def timed(K, **kw):
         barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+        e0.record(ms_stream)
         for k in range(K):
             step(k, **kw)
-        e1.record(stream)
+        e1.record(ms_stream)
         torch.cuda.synchronize()
         barrier()
         return multi.max_over_ranks(e0.elapsed_time(e1), ws, dev)
@@ -1287,8 +1279,10 @@ def run_dit_job(args, dev, rank, ws, local, stream):
     peaks, kind = measured_peaks()
     fl = dit_step_flops(cfg, Ng, S, enc_S)
     out = {}
-    for mode in ("fast", "exact"):  # the headline mode last, so its graphs are the live ones
+    x0_all = np.empty((N, T, Oc), np.float32)
+    for mode in ("fast", "exact"):  # the headline mode last
         dit.set_exact(mode == "exact")
+        job_begin()
         for k in range(max(args.warmup, 3)):
             step(k)
         K = args.steps if mode == "exact" else min(args.steps, DIT_STEPS)
@@ -1298,6 +1292,15 @@ def run_dit_job(args, dev, rank, ws, local, stream):
             time.sleep(0.3)
         ms = timed(K)
         clocks = clk.stop() if clk else None
+        if mode == "exact":
+            # end to end: the same steps through the C ABI with this rank's step result (xt, or x0 at
+            # the last step) read back to pinned host memory every step (the step's t values go up
+            # from the host inside every acb_dit_job_step)
+            n_tr_loc = 1 if half >= 0 else n_loc_tr
+            h_out = torch.empty((n_tr_loc, T, Oc), dtype=torch.float32, pin_memory=True)
+            e2e_k = DIT_STEPS
+            e2e_ms = timed(e2e_k, h_out=h_out)
+        acb._check("acb_dit_job_end", L.acb_dit_job_end(dit.h, x0_all.ctypes.data, None))
         step_ms = ms / K
         out[mode] = {"value": round(K / (ms * 1e-3), 3), "ms_per_step": round(step_ms, 3), "steps": K,
                      "clocks": clocks,
@@ -1308,13 +1311,6 @@ def run_dit_job(args, dev, rank, ws, local, stream):
                                   "frac": round(fl / ws / (step_ms * 1e-3) / 1e12 / peaks["bf16_tflops_sustained"], 4),
                                   "traffic": None, "tensor_work_multiplier": 3 if mode == "exact" else 1}}
     dom = dominant_gemm(dev, n_loc * S, 2 * cfg["intermediate_size"], cfg["hidden_size"], peaks, kind)
-    # end to end: the same steps with the timestep row copied in from pinned host memory and the
-    # step's result (xt, or x0 at the last step) read back to pinned host memory every step
-    h_tts = torch.empty((DIT_STEPS, 3), dtype=torch.float32, pin_memory=True).copy_(tts)
-    d_tt = torch.empty(3, dtype=torch.float32, device=dev)
-    h_out = torch.empty((N, T, Oc), dtype=torch.float32, pin_memory=True)
-    e2e_k = DIT_STEPS
-    e2e_ms = timed(e2e_k, h_tt=(h_tts, d_tt), h_out=h_out)
     ex = out["exact"]
     launches = dit.eval_kernels() + 2  # evaluation graph + APG + Euler per step
     line = {"metric": "DiT denoise steps/s (config 4: 24 layers, hidden 2048, Q8_0, 4 tracks x CFG 2 = 8 "
@@ -1327,20 +1323,25 @@ def run_dit_job(args, dev, rank, ws, local, stream):
             "config": {"workload": "config4_dit2b_q8_0_turbo_cfg", "tracks": N, "sequences": Ng,
                        "sequences_per_gpu": n_loc, "frames": T, "tokens": S, "enc_rows": enc_S,
                        "schedule": "turbo shift 3, 8 steps (cycled)", "guidance": DIT_GUIDANCE,
-                       "parallelism": f"sequence-sharded dp{ws}, NCCL all-gather of velocities per step"
-                                      if ws > 1 else "single",
+                       "parallelism": ("one CFG half per GPU, NCCL velocity exchange per step (acb_dit_job_*)"
+                                       if half >= 0 else f"track pairs per GPU ({n_loc_tr}), no per-step exchange "
+                                       "(acb_dit_job_*)") if ws > 1 else "single",
                        "l2": "weights 9.4 GB and activations > 126 MB L2: every step streams from HBM",
                        "flops_per_step": fl},
             "roofline": dom["roofline"], "step_roofline": ex["roofline"], "dominant_kernel": dom["detail"],
             "clocks": ex["clocks"],
             "e2e": {"value": round(e2e_k / (e2e_ms * 1e-3), 3), "unit": "step/s", "h2d_bytes_per_step": 12,
-                    "d2h_bytes_per_step": N * T * Oc * 4,
-                    "path": "acb_dit_eval + acb_dit_apg + acb_dit_euler with per-step pinned host copies"},
+                    "d2h_bytes_per_step": int(h_out.numel() * 4),
+                    "path": "acb_dit_job_step with the step's times from the host and its result to pinned host "
+                            "memory every step"},
             "gpu_launches": launches * ex["steps"],
+            "x0_finite": bool(np.isfinite(x0_all).all()),
             "fast_mode": {k: out["fast"][k] for k in ("value", "ms_per_step", "roofline")}}
     if keep is not None:
         line["cpu_baseline"] = cpu_dit_sample(cfg, keep, N, T, enc_S)
     dit.close()
+    if comm:
+        comm.close()
     del keep
     torch.cuda.empty_cache()
     return line

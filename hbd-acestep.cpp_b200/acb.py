@@ -19,7 +19,7 @@ HEADER_DIR = os.path.join(ROOT, "include")
 F32, F16, Q8_0, Q4_K, Q6_K, Q8_K, I32, BF16 = 0, 1, 8, 12, 14, 15, 26, 30
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "unsupported", 3: "cuda error", 4: "out of range", 5: "oom",
-          6: "io", 7: "format", 8: "device error flag", 9: "cancelled"}
+          6: "io", 7: "format", 8: "device error flag", 9: "cancelled", 10: "timeout"}
 
 
 class AcbError(RuntimeError):
@@ -111,6 +111,18 @@ def lib():
             "acb_dit_generate_ex": (I, [P, P, P, P, I, I, I, I, P, P, F, P, I, P, P, P, P, P, P, P, I, F, F,
                                         C.c_char_p, C.c_char_p, I, P, P, P]),
             "acb_dit_set_lengths": (I, [P, P, P, P]),
+            "acb_comm_unique_id": (I, [P]),
+            "acb_comm_init": (I, [P, I, I, I, I, C.POINTER(C.c_void_p)]),
+            "acb_comm_rank": (I, [P]),
+            "acb_comm_world": (I, [P]),
+            "acb_comm_free": (None, [P]),
+            "acb_dit_shard_plan": (I, [I, I, I, I, C.POINTER(I), C.POINTER(I), C.POINTER(I), C.POINTER(I)]),
+            "acb_dit_generate_sharded": (I, [P, P, P, P, P, I, I, I, I, P, P, F, P, I, P, P, P, P, P, P, P,
+                                             C.c_char_p, P, P, P]),
+            "acb_dit_job_begin": (I, [P, P, P, P, P, I, I, I, F, P, I, P, P, P, P, P, P, P, C.c_char_p, P, P]),
+            "acb_dit_job_step": (I, [P, I, F, F, I, P]),
+            "acb_dit_job_end": (I, [P, P, P]),
+            "acb_dit_stream": (P, [P]),
             "acb_dit_free": (None, [P]),
             "acb_dit_set_condition": (I, [P, P, I, I, I, P]),
             "acb_attn_tc": (I, [P, I64, P, I64, P, I64, P, I, I64, I, I, I, I, I, I, I, I, I, F, I, I64, I64, I64, P,
@@ -789,6 +801,62 @@ class DiT:
             sched.ctypes.data, out.ctypes.data, float(guidance_scale), self.SOLVERS[solver],
             C.cast(C.pointer(ms), C.c_void_p)))
         return out, ms.value
+
+
+class Comm:
+    """acb_comm: the library's NCCL communicator (one process per GPU)."""
+
+    def __init__(self, uid: bytes, world: int, rank: int, device: int = 0, timeout_ms: int = 60000):
+        h = C.c_void_p()
+        buf = C.create_string_buffer(bytes(uid), 128)
+        _check("acb_comm_init", lib().acb_comm_init(buf, world, rank, device, timeout_ms, C.byref(h)))
+        self.h = h
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        _check("acb_comm_unique_id", lib().acb_comm_unique_id(buf))
+        return buf.raw
+
+    def close(self):
+        if self.h:
+            lib().acb_comm_free(self.h)
+            self.h = None
+
+
+def dit_shard_plan(n_tracks, cfg, world, rank):
+    """(track0, n_local, half, peer) of acb_dit_shard_plan."""
+    v = [C.c_int() for _ in range(4)]
+    _check("acb_dit_shard_plan", lib().acb_dit_shard_plan(n_tracks, int(cfg), world, rank, *[C.byref(x) for x in v]))
+    return tuple(x.value for x in v)
+
+
+def dit_generate_sharded(dit, comm, noise, context, enc, schedule, guidance_scale=1.0, solver="euler", real_S=None,
+                         real_enc_S=None, seeds=None, randn=None):
+    """acb_dit_generate_sharded: every rank passes the whole job, every rank gets every track's x0."""
+    import numpy as np
+    f32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.float32)
+    i32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.int32)
+    ptr = lambda a: None if a is None else a.ctypes.data
+    noise, context, enc = f32(noise), f32(context), f32(enc)
+    rs, re = i32(real_S), i32(real_enc_S)
+    sd = None if seeds is None else np.ascontiguousarray(seeds, dtype=np.int64)
+    sched = np.ascontiguousarray(schedule, dtype=np.float32)
+    N, T, _ = noise.shape
+    out = np.empty_like(noise)
+    ms = C.c_float(0.0)
+    RANDN = C.CFUNCTYPE(None, C.c_int64, C.POINTER(C.c_float), C.c_int, C.c_void_p)
+
+    def _randn(seed, outp, n, _):
+        v = np.ascontiguousarray(randn(int(seed), int(n)), dtype=np.float32)
+        C.memmove(outp, v.ctypes.data, 4 * int(n))
+
+    cb_r = RANDN(_randn) if randn is not None else None
+    _check("acb_dit_generate_sharded", lib().acb_dit_generate_sharded(
+        dit.h, comm.h, noise.ctypes.data, context.ctypes.data, enc.ctypes.data, enc.shape[1], T, N, sched.size,
+        sched.ctypes.data, out.ctypes.data, float(guidance_scale), None, -1, None, None, ptr(rs), ptr(re), None, None,
+        ptr(sd), solver.encode(), C.cast(cb_r, C.c_void_p) if cb_r else None, None, C.cast(C.pointer(ms), C.c_void_p)))
+    return out, ms.value
 
 
 def turbo_schedule(steps=8, shift=3.0):

@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "../../include/acb_models.h"
+#include "comm.h"
 #include "dense.h"
 #include "gguf.h"
 #include "host_common.h"
@@ -51,6 +52,8 @@ struct TembW {
 constexpr int kPdl = ACB_FLAG_PDL;
 
 }  // namespace
+
+struct DiTRun;
 
 struct acb_dit {
     int            device = 0;
@@ -83,15 +86,11 @@ struct acb_dit {
     DevBuf                          xt, vt, out, ra;
     DevBuf                          hist1, hist2;  // DPM++ 3M velocity history (previous, the one before)
     DevBuf                          noise;         // SDE: the step's fresh noise [N][T][out_ch]
+    DevBuf                          vpair, xall;   // sharded: [cond, uncond] velocities; gathered x0
+    std::unique_ptr<DiTRun>         job;           // the step-level job (acb_dit_job_*)
     std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
 
-    ~acb_dit() {
-        cudaSetDevice(device);
-        drop_graphs();
-        if (st) {
-            cudaStreamDestroy(st);
-        }
-    }
+    ~acb_dit();
 
     void drop_graphs() {
         for (auto & kv : graphs) {
@@ -889,43 +888,132 @@ struct GenArgs {
     float *         gpu_ms            = nullptr;
 };
 
-acb_status generate_impl(acb_dit * m, const GenArgs & g) {
-    const int  N = g.N, T = g.T, enc_S = g.enc_S, num_steps = g.num_steps;
+}  // namespace
+
+// One denoise run on this model: the whole job (tracks [0, N)), or this rank's share of a sharded
+// job -- whole track pairs (half = -1), or one CFG half of one track (half = 0 conditional, 1
+// unconditional) whose partner rank holds the other half. Host argument pointers are the job's;
+// the run reads the tracks [track0, track0 + n) of them.
+struct DiTRun {
+    acb_dit *   m      = nullptr;
+    acb_comm *  comm   = nullptr;
+    GenArgs     g;
+    int         track0 = 0, n = 0;  // local tracks
+    int         half   = -1;        // -1 whole pairs; 0 / 1 one half of track track0
+    int         peer   = -1;        // the partner rank in half mode
+    bool        do_cfg = false;
+    int         Ng     = 0;         // local slots
+    int         T = 0, Oc = 0, in_ch = 0, ctx_ch = 0, He = 0, enc_S = 0;
+    size_t      n_per  = 0, n_tot = 0;
+    std::vector<float> nul;
+    std::vector<int>   re_now, re_first;
+    std::vector<float> tv, fresh;
+    bool        switched = false, began = false;
+    cudaStream_t s = nullptr;
+    cudaEvent_t  e0 = nullptr, e1 = nullptr, done[2] = { nullptr, nullptr };
+    int          steps_run = 0;
+
+    ~DiTRun() {
+        for (cudaEvent_t e : { e0, e1, done[0], done[1] }) {
+            if (e) {
+                cudaEventDestroy(e);
+            }
+        }
+    }
+
+    const float * ctx_of(const float * c) const { return c + (size_t) track0 * T * ctx_ch; }
+    const float * enc_of(const float * e) const { return e + (size_t) track0 * enc_S * He; }
+
+    bool upload_context(const float * ctx) {
+        std::vector<float> in((size_t) Ng * T * in_ch, 0.0f);
+        for (int b = 0; b < Ng; b++) {
+            const int src = b % n;
+            for (int t = 0; t < T; t++) {
+                memcpy(&in[((size_t) b * T + t) * in_ch], &ctx_of(ctx)[((size_t) src * T + t) * ctx_ch],
+                       (size_t) ctx_ch * 4);
+            }
+        }
+        return cudaMemcpyAsync(m->input.p, in.data(), in.size() * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+               cudaStreamSynchronize(s) == cudaSuccess;
+    }
+
+    // slot b < n is track b's conditional slot (or, in half mode, the one slot of this half)
+    bool slot_is_null(int b) const { return half >= 0 ? half == 1 : b >= n; }
+
+    bool upload_enc(const float * e) {
+        std::vector<float> enc((size_t) Ng * enc_S * He);
+        for (int b = 0; b < Ng; b++) {
+            float * dst = &enc[(size_t) b * enc_S * He];
+            if (slot_is_null(b)) {
+                for (int r = 0; r < enc_S; r++) {
+                    memcpy(dst + (size_t) r * He, nul.data(), (size_t) He * 4);
+                }
+            } else {
+                memcpy(dst, enc_of(e) + (size_t) (b % n) * enc_S * He, (size_t) enc_S * He * 4);
+            }
+        }
+        return cudaMemcpyAsync(m->enc_in.p, enc.data(), enc.size() * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
+               cudaStreamSynchronize(s) == cudaSuccess;
+    }
+
+    // padding (dit-sampler.h:244-304): every slot takes its track's lengths; the conditional slots
+    // follow a cover switch, the unconditional ones keep the first lengths
+    acb_status upload_lengths() {
+        std::vector<int> rs((size_t) Ng), re((size_t) Ng);
+        for (int b = 0; b < Ng; b++) {
+            const int tr   = b % n;
+            rs[(size_t) b] = g.real_S ? g.real_S[track0 + tr] : m->S;
+            re[(size_t) b] = slot_is_null(b) ? re_first[(size_t) tr] : re_now[(size_t) tr];
+        }
+        return m->set_lengths(rs.data(), re.data(), Ng, s);
+    }
+
+    acb_status begin(acb_dit * model, acb_comm * c, const GenArgs & args, int t0, int nloc, int h, int pr);
+    acb_status get_graph(int first, int last, int hist, int part, cudaGraphExec_t * ex);
+    acb_status step(int step, float t_curr, float t_next, bool last, float * host_out);
+    acb_status finish(float * host_out, bool gather);
+};
+
+acb_status DiTRun::begin(acb_dit * model, acb_comm * c, const GenArgs & args, int t0, int nloc, int h, int pr) {
+    m = model, comm = c, g = args, track0 = t0, n = nloc, half = h, peer = pr;
     const bool dpm = g.solver == ACB_SOLVER_DPM3M, sde = g.solver == ACB_SOLVER_SDE;
-    if (!m || !g.noise || !g.context || !g.enc || !g.schedule || !g.output || N <= 0 || T <= 0 || enc_S <= 0 ||
-        num_steps <= 0 || T % m->c.patch_size != 0 ||
+    if (!m || !g.noise || !g.context || !g.enc || g.N <= 0 || g.T <= 0 || g.enc_S <= 0 || n <= 0 ||
+        g.T % m->c.patch_size != 0 ||
         (g.solver != ACB_SOLVER_EULER && g.solver != ACB_SOLVER_DPM3M && g.solver != ACB_SOLVER_SDE) ||
-        (sde && (!g.seeds || !g.randn))) {
+        (sde && (!g.seeds || !g.randn)) || (half >= 0 && (n != 1 || !comm))) {
         return ACB_ERR_INVALID_ARG;
     }
     if (cudaSetDevice(m->device) != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
-    const acb_dit_config & c      = m->c;
-    const int              Oc     = c.out_channels;
-    const int              in_ch  = c.in_channels, ctx_ch = in_ch - Oc;
-    const int              He     = c.enc_hidden_size;
-    // CFG batching (dit-sampler.h:167-171): conditional slots [0, N), unconditional [N, 2N)
-    const bool do_cfg = g.guidance > 1.0f && m->null_emb;
-    const int  Ng     = do_cfg ? 2 * N : N;
+    const acb_dit_config & cf = m->c;
+    T = g.T, enc_S = g.enc_S, Oc = cf.out_channels, in_ch = cf.in_channels, ctx_ch = in_ch - Oc;
+    He = cf.enc_hidden_size;
+    // CFG batching (dit-sampler.h:167-171): conditional slots [0, n), unconditional [n, 2n); in half
+    // mode this rank evaluates one of them
+    do_cfg = g.guidance > 1.0f && m->null_emb;
+    if (half >= 0 && !do_cfg) {
+        set_last_error("a rank per CFG half needs guidance > 1 and a null condition");
+        return ACB_ERR_INVALID_ARG;
+    }
+    Ng = half >= 0 ? 1 : (do_cfg ? 2 * n : n);
     ACB_TRY(m->reserve(Ng, T, enc_S));
-    cudaStream_t s     = m->st;
-    const size_t n_per = (size_t) T * Oc, n_tot = n_per * N;
-    bool         bad   = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
-                 m->ra.bytes < n_tot * 8 || (dpm && (m->hist1.bytes < n_tot * 4 || m->hist2.bytes < n_tot * 4)) ||
-                 (sde && m->noise.bytes < n_tot * 4);
+    s     = m->st;
+    n_per = (size_t) T * Oc, n_tot = n_per * n;
+    const size_t pair = half >= 0 ? 2 * n_per : 0;  // [cond, uncond] velocities of the track
+    bool bad = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
+               m->ra.bytes < n_tot * 8 || (dpm && (m->hist1.bytes < n_tot * 4 || m->hist2.bytes < n_tot * 4)) ||
+               (sde && m->noise.bytes < n_tot * 4) || m->vpair.bytes < pair * 4;
     if (bad) {
         m->drop_graphs();  // the graphs hold these addresses
         if (m->xt.alloc(n_tot * 4) != ACB_OK || m->vt.alloc(n_tot * 4) != ACB_OK || m->out.alloc(n_tot * 4) != ACB_OK ||
             m->ra.alloc(n_tot * 8) != ACB_OK ||
             (dpm && (m->hist1.alloc(n_tot * 4) != ACB_OK || m->hist2.alloc(n_tot * 4) != ACB_OK)) ||
-            (sde && m->noise.alloc(n_tot * 4) != ACB_OK)) {
+            (sde && m->noise.alloc(n_tot * 4) != ACB_OK) || (pair && m->vpair.alloc(pair * 4) != ACB_OK)) {
             set_last_error("DiT generate buffers allocation failed");
             return ACB_ERR_OOM;
         }
     }
-    // inputs: context channels of every slot (uncond mirrors cond), the noise, the condition
-    std::vector<float> nul;
     if (do_cfg) {
         // null_condition_emb broadcast over enc_S rows for the unconditional slots (:345-385)
         if (m->null_emb->type != ACB_TYPE_F32 || m->null_emb->K * m->null_emb->N != He) {
@@ -935,192 +1023,259 @@ acb_status generate_impl(acb_dit * m, const GenArgs & g) {
         nul.resize((size_t) He);
         cudaMemcpy(nul.data(), m->null_emb->data, (size_t) He * 4, cudaMemcpyDeviceToHost);
     }
-    auto upload_context = [&](const float * ctx) -> bool {
-        std::vector<float> in((size_t) Ng * T * in_ch, 0.0f);
-        for (int b = 0; b < Ng; b++) {
-            const int src = b % N;
-            for (int t = 0; t < T; t++) {
-                memcpy(&in[((size_t) b * T + t) * in_ch], &ctx[((size_t) src * T + t) * ctx_ch], (size_t) ctx_ch * 4);
-            }
-        }
-        return cudaMemcpyAsync(m->input.p, in.data(), in.size() * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
-               cudaStreamSynchronize(s) == cudaSuccess;
-    };
-    auto upload_enc = [&](const float * e) -> bool {
-        std::vector<float> enc((size_t) Ng * enc_S * He);
-        memcpy(enc.data(), e, (size_t) N * enc_S * He * 4);
-        for (int b = N; b < Ng; b++) {
-            for (int r = 0; r < enc_S; r++) {
-                memcpy(&enc[((size_t) b * enc_S + r) * He], nul.data(), (size_t) He * 4);
-            }
-        }
-        return cudaMemcpyAsync(m->enc_in.p, enc.data(), enc.size() * 4, cudaMemcpyHostToDevice, s) == cudaSuccess &&
-               cudaStreamSynchronize(s) == cudaSuccess;
-    };
-    // padding (dit-sampler.h:244-304): slot b < N uses track b's lengths, its CFG twin the same
-    std::vector<int> re_now((size_t) N, enc_S);
+    re_now.assign((size_t) n, enc_S);
     if (g.real_enc_S) {
-        re_now.assign(g.real_enc_S, g.real_enc_S + N);
+        re_now.assign(g.real_enc_S + track0, g.real_enc_S + track0 + n);
     }
-    auto upload_lengths = [&](const int * re_cond, const int * re_uncond) -> acb_status {
-        std::vector<int> rs((size_t) Ng), re((size_t) Ng);
-        for (int b = 0; b < Ng; b++) {
-            rs[(size_t) b] = g.real_S ? g.real_S[b % N] : m->S;
-            re[(size_t) b] = b < N ? re_cond[b] : re_uncond[b - N];
-        }
-        return m->set_lengths(rs.data(), re.data(), Ng, s);
-    };
+    re_first = re_now;
     if (!upload_context(g.context) || !upload_enc(g.enc) ||
-        cudaMemcpyAsync(m->xt.p, g.noise, n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        cudaMemcpyAsync(m->xt.p, g.noise + (size_t) track0 * n_per, n_tot * 4, cudaMemcpyHostToDevice, s) !=
+            cudaSuccess) {
         return ACB_ERR_CUDA;
     }
-    const std::vector<int> re_first = re_now;
-    ACB_TRY(upload_lengths(re_now.data(), re_first.data()));
+    ACB_TRY(upload_lengths());
     ACB_TRY(m->condition(s));
-
-    // one graph per (shape, cfg, first, last, solver, history): pack xt, evaluate, guidance, then the
-    // solver step (Euler, DPM++ 3M with min(step, 2) stored velocities, SDE with the step's noise)
-    // or the last step's x0
-    auto get_graph = [&](int first, int last, int hist, cudaGraphExec_t * ex) -> acb_status {
-        uint32_t gbits = 0;  // the guidance scale is baked into the captured APG launch
-        memcpy(&gbits, &g.guidance, 4);
-        const int  stepk = (g.solver * 3 + hist) * 4 + first * 2 + last;
-        const auto key   = std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, stepk, m->exact ? 1 : 0, gbits);
-        auto       it  = m->graphs.find(key);
-        if (it != m->graphs.end()) {
-            *ex = it->second;
-            return ACB_OK;
-        }
-        cudaGraph_t gr = nullptr;
-        if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-            return ACB_ERR_CUDA;
-        }
-        acb_status st = acb_dit_pack_xt(m->xt.as<float>(), m->input.as<float>(), N, Ng, T, Oc, ctx_ch, (acb_stream_t) s);
-        if (st == ACB_OK) {
-            st = m->evaluate(-1, s);
-        }
-        float * v = m->vel.as<float>();
-        if (st == ACB_OK && do_cfg) {
-            st = acb_dit_apg(v, v + n_tot, m->ra.as<double>(), first, -0.75f, g.guidance, 2.5f, N, T, Oc,
-                             m->vt.as<float>(), (acb_stream_t) s);
-            v  = m->vt.as<float>();
-        }
-        if (st == ACB_OK && dpm && !last) {
-            st = acb_dit_dpm3m(m->xt.as<float>(), v, m->hist1.as<float>(), m->hist2.as<float>(), hist,
-                               m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
-        } else if (st == ACB_OK && sde && !last) {
-            st = acb_dit_sde(m->xt.as<float>(), v, m->noise.as<float>(), m->tt.as<float>(), (int64_t) n_tot,
-                             (acb_stream_t) s);
-        } else if (st == ACB_OK) {
-            st = acb_dit_euler(m->xt.as<float>(), v, m->tt.as<float>(), last, m->out.as<float>(), (int64_t) n_tot,
-                               (acb_stream_t) s);
-        }
-        const cudaError_t ce = cudaStreamEndCapture(s, &gr);
-        if (st != ACB_OK || ce != cudaSuccess) {
-            if (gr) {
-                cudaGraphDestroy(gr);
-            }
-            set_last_error("DiT step graph capture failed");
-            return st != ACB_OK ? st : ACB_ERR_CUDA;
-        }
-        const cudaError_t ie = cudaGraphInstantiate(ex, gr, 0);
-        cudaGraphDestroy(gr);
-        if (ie != cudaSuccess) {
-            return ACB_ERR_CUDA;
-        }
-        m->graphs.emplace(key, *ex);
-        return ACB_OK;
-    };
-    cudaEvent_t e0 = nullptr, e1 = nullptr, done[2] = { nullptr, nullptr };
+    fresh.assign(sde ? n_tot : 0, 0.0f);
+    tv.assign(3, 0.0f);
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming);
     cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming);
-    acb_status         st = ACB_OK;
-    std::vector<float> tv((size_t) num_steps * 3);
-    std::vector<float> fresh(sde ? n_tot : 0);
-    bool               switched = false;
-    for (int step = 0; step < num_steps && st == ACB_OK; step++) {
-        // at most two steps in flight, so that a cancellation (polled before every step, like
-        // dit-sampler.h:409-413) takes effect within two steps
-        if (step >= 2 && cudaEventSynchronize(done[step & 1]) != cudaSuccess) {
-            st = ACB_ERR_CUDA;
-            break;
-        }
-        if (g.cancel && g.cancel(g.cancel_data)) {
-            cudaStreamSynchronize(s);
-            set_last_error("cancelled at step " + std::to_string(step) + "/" + std::to_string(num_steps));
-            st = ACB_ERR_CANCELLED;
-            break;
-        }
-        // cover mode (dit-sampler.h:414-449): from cover_steps on, the other context (every slot)
-        // and, for the conditional slots, the other condition and its lengths
-        if (g.context_switch && g.cover_steps >= 0 && step >= g.cover_steps && !switched) {
-            switched = true;
-            if (cudaStreamSynchronize(s) != cudaSuccess || !upload_context(g.context_switch)) {
-                st = ACB_ERR_CUDA;
-                break;
-            }
-            if (g.enc_switch) {
-                if (g.real_enc_S_switch) {
-                    re_now.assign(g.real_enc_S_switch, g.real_enc_S_switch + N);
-                }
-                if (!upload_enc(g.enc_switch) || upload_lengths(re_now.data(), re_first.data()) != ACB_OK ||
-                    m->condition(s) != ACB_OK) {
-                    st = ACB_ERR_CUDA;
-                    break;
-                }
-            }
-        }
-        const int       first = step == 0, last = step == num_steps - 1;
-        cudaGraphExec_t ex    = nullptr;
-        st                    = get_graph(first, last, dpm ? (step < 2 ? step : 2) : 0, &ex);
-        if (st != ACB_OK) {
-            break;
-        }
-        // SDE: the fresh noise of every track from its seed (solver-sde.h:28-31: seed_b + step + 1)
-        if (sde && !last) {
-            for (int b = 0; b < N; b++) {
-                g.randn(g.seeds[b] + step + 1, fresh.data() + (size_t) b * n_per, (int) n_per, g.randn_data);
-            }
-            if (cudaMemcpyAsync(m->noise.p, fresh.data(), n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
-                st = ACB_ERR_CUDA;
-                break;
-            }
-        }
-        // t_curr, t_r = t_curr (dit-sampler.h:431-436), t_next
-        float * t3 = &tv[(size_t) step * 3];
-        t3[0]      = g.schedule[step];
-        t3[1]      = g.schedule[step];
-        t3[2]      = last ? 0.0f : g.schedule[step + 1];
-        if (step == 0) {
-            cudaEventRecord(e0, s);
-        }
-        if (cudaMemcpyAsync(m->tt.p, t3, 3 * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess ||
-            cudaGraphLaunch(ex, s) != cudaSuccess || cudaEventRecord(done[step & 1], s) != cudaSuccess) {
-            st = ACB_ERR_CUDA;
+    switched = false, began = true, steps_run = 0;
+    return ACB_OK;
+}
+
+// Step graphs, one per (shape, cfg, mode, first, last, solver, history, part): part 0 is the whole
+// step (pack xt, evaluate, guidance, solver); in half mode part 1 is pack + evaluate and part 2
+// guidance + solver, with the exchange of the velocity between them.
+acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphExec_t * ex) {
+    const bool dpm = g.solver == ACB_SOLVER_DPM3M, sde = g.solver == ACB_SOLVER_SDE;
+    uint32_t   gbits = 0;  // the guidance scale is baked into the captured APG launch
+    memcpy(&gbits, &g.guidance, 4);
+    const int  stepk = (((g.solver * 3 + hist) * 4 + first * 2 + last) * 4 + part) * 3 + (half + 1);
+    const auto key   = std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, stepk, m->exact ? 1 : 0, gbits);
+    auto       it    = m->graphs.find(key);
+    if (it != m->graphs.end()) {
+        *ex = it->second;
+        return ACB_OK;
+    }
+    cudaGraph_t gr = nullptr;
+    if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    acb_status st = ACB_OK;
+    if (part != 2) {
+        st = acb_dit_pack_xt(m->xt.as<float>(), m->input.as<float>(), n, Ng, T, Oc, ctx_ch, (acb_stream_t) s);
+        if (st == ACB_OK) {
+            st = m->evaluate(-1, s);
         }
     }
+    if (part != 1) {
+        const float * v = m->vel.as<float>();
+        if (st == ACB_OK && do_cfg) {
+            // guidance on [cond, uncond]: the two halves of the slots, or (half mode) of the pair
+            // buffer the exchange filled
+            const float * vc = half >= 0 ? m->vpair.as<float>() : v;
+            st = acb_dit_apg(vc, vc + n_tot, m->ra.as<double>(), first, -0.75f, g.guidance, 2.5f, n, T, Oc,
+                             m->vt.as<float>(), (acb_stream_t) s);
+            v  = m->vt.as<float>();
+        }
+        float * vv = const_cast<float *>(v);
+        if (st == ACB_OK && dpm && !last) {
+            st = acb_dit_dpm3m(m->xt.as<float>(), vv, m->hist1.as<float>(), m->hist2.as<float>(), hist,
+                               m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
+        } else if (st == ACB_OK && sde && !last) {
+            st = acb_dit_sde(m->xt.as<float>(), vv, m->noise.as<float>(), m->tt.as<float>(), (int64_t) n_tot,
+                             (acb_stream_t) s);
+        } else if (st == ACB_OK) {
+            st = acb_dit_euler(m->xt.as<float>(), vv, m->tt.as<float>(), last, m->out.as<float>(), (int64_t) n_tot,
+                               (acb_stream_t) s);
+        }
+    }
+    const cudaError_t ce = cudaStreamEndCapture(s, &gr);
+    if (st != ACB_OK || ce != cudaSuccess) {
+        if (gr) {
+            cudaGraphDestroy(gr);
+        }
+        set_last_error("DiT step graph capture failed");
+        return st != ACB_OK ? st : ACB_ERR_CUDA;
+    }
+    const cudaError_t ie = cudaGraphInstantiate(ex, gr, 0);
+    cudaGraphDestroy(gr);
+    if (ie != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    m->graphs.emplace(key, *ex);
+    return ACB_OK;
+}
+
+acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * host_out) {
+    if (!began) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const bool dpm = g.solver == ACB_SOLVER_DPM3M, sde = g.solver == ACB_SOLVER_SDE;
+    // at most two steps in flight, so that a cancellation (polled before every step, like
+    // dit-sampler.h:409-413) takes effect within two steps
+    if (steps_run >= 2 && cudaEventSynchronize(done[steps_run & 1]) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    if (g.cancel && g.cancel(g.cancel_data)) {
+        cudaStreamSynchronize(s);
+        set_last_error("cancelled at step " + std::to_string(k));
+        return ACB_ERR_CANCELLED;
+    }
+    // cover mode (dit-sampler.h:414-449): from cover_steps on, the other context (every slot) and,
+    // for the conditional slots, the other condition and its lengths
+    if (g.context_switch && g.cover_steps >= 0 && k >= g.cover_steps && !switched) {
+        switched = true;
+        if (cudaStreamSynchronize(s) != cudaSuccess || !upload_context(g.context_switch)) {
+            return ACB_ERR_CUDA;
+        }
+        if (g.enc_switch) {
+            if (g.real_enc_S_switch) {
+                re_now.assign(g.real_enc_S_switch + track0, g.real_enc_S_switch + track0 + n);
+            }
+            if (!upload_enc(g.enc_switch) || upload_lengths() != ACB_OK || m->condition(s) != ACB_OK) {
+                return ACB_ERR_CUDA;
+            }
+        }
+    }
+    const int first = k == 0 ? 1 : 0, lst = last ? 1 : 0, hist = dpm ? (k < 2 ? k : 2) : 0;
+    // SDE: the fresh noise of every track from its seed (solver-sde.h:28-31: seed_b + step + 1)
+    if (sde && !last) {
+        for (int b = 0; b < n; b++) {
+            g.randn(g.seeds[track0 + b] + k + 1, fresh.data() + (size_t) b * n_per, (int) n_per, g.randn_data);
+        }
+        if (cudaMemcpyAsync(m->noise.p, fresh.data(), n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+    }
+    // t_curr, t_r = t_curr (dit-sampler.h:431-436), t_next; pageable source: staged by the call
+    tv[0] = t_curr, tv[1] = t_curr, tv[2] = last ? 0.0f : t_next;
+    if (steps_run == 0) {
+        cudaEventRecord(e0, s);
+    }
+    if (cudaMemcpyAsync(m->tt.p, tv.data(), 3 * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    if (half < 0) {
+        cudaGraphExec_t ex = nullptr;
+        ACB_TRY(get_graph(first, lst, hist, 0, &ex));
+        if (cudaGraphLaunch(ex, s) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+    } else {
+        // evaluate this half, swap velocities with the partner, then guidance + solver on the
+        // [cond, uncond] pair (both ranks of the pair hold the same xt and take the same step)
+        cudaGraphExec_t ea = nullptr, eb = nullptr;
+        ACB_TRY(get_graph(first, lst, hist, 1, &ea));
+        ACB_TRY(get_graph(first, lst, hist, 2, &eb));
+        float * mine  = m->vpair.as<float>() + (size_t) half * n_per;
+        float * other = m->vpair.as<float>() + (size_t) (1 - half) * n_per;
+        if (cudaGraphLaunch(ea, s) != cudaSuccess ||
+            cudaMemcpyAsync(mine, m->vel.p, n_per * 4, cudaMemcpyDeviceToDevice, s) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+        ACB_TRY(comm_exchange(comm, peer, mine, other, n_per * 4, s));
+        if (cudaGraphLaunch(eb, s) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+    }
+    if (host_out && cudaMemcpyAsync(host_out, last ? m->out.p : m->xt.p, n_tot * 4, cudaMemcpyDeviceToHost, s) !=
+                        cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    if (cudaEventRecord(done[steps_run & 1], s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    steps_run++;
+    return ACB_OK;
+}
+
+// x0 of the run's tracks (the last step's prediction) to host_out: this rank's tracks, or with
+// `gather` every rank's, all-gathered in rank order (track order) over the communicator.
+acb_status DiTRun::finish(float * host_out, bool gather) {
+    if (!began) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    began = false;
     cudaEventRecord(e1, s);
-    int dev_err = 0;
-    if (st == ACB_OK && (cudaMemcpyAsync(g.output, m->out.p, n_tot * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-                         cudaMemcpyAsync(&dev_err, m->err.p, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-                         cudaStreamSynchronize(s) != cudaSuccess)) {
-        st = ACB_ERR_CUDA;
+    const float * src = m->out.as<float>();
+    size_t        cnt = n_tot;
+    if (gather && comm) {
+        const int w = comm_world(comm);
+        if (half >= 0) {
+            // both ranks of a pair hold the track's x0: gather every rank's copy, keep even ranks'
+            if (m->xall.bytes < (size_t) w * n_tot * 4) {
+                ACB_TRY(m->xall.alloc((size_t) w * n_tot * 4));
+            }
+            ACB_TRY(comm_all_gather(comm, m->out.p, m->xall.p, n_tot * 4, s));
+            ACB_TRY(comm_wait(comm, s));
+            std::vector<float> all((size_t) w * n_tot);
+            if (cudaMemcpy(all.data(), m->xall.p, all.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+                return ACB_ERR_CUDA;
+            }
+            for (int r = 0; r < w; r += 2) {
+                memcpy(host_out + (size_t) (r / 2) * n_tot, all.data() + (size_t) r * n_tot, n_tot * 4);
+            }
+            src = nullptr;
+        } else {
+            if (m->xall.bytes < (size_t) w * n_tot * 4) {
+                ACB_TRY(m->xall.alloc((size_t) w * n_tot * 4));
+            }
+            ACB_TRY(comm_all_gather(comm, m->out.p, m->xall.p, n_tot * 4, s));
+            ACB_TRY(comm_wait(comm, s));
+            src = m->xall.as<float>();
+            cnt = (size_t) w * n_tot;
+        }
     }
-    cudaStreamSynchronize(s);
-    if (st == ACB_OK && g.gpu_ms) {
+    int dev_err = 0;
+    if ((src && cudaMemcpyAsync(host_out, src, cnt * 4, cudaMemcpyDeviceToHost, s) != cudaSuccess) ||
+        cudaMemcpyAsync(&dev_err, m->err.p, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    if (g.gpu_ms) {
         cudaEventElapsedTime(g.gpu_ms, e0, e1);
     }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    cudaEventDestroy(done[0]);
-    cudaEventDestroy(done[1]);
-    if (st == ACB_OK && dev_err) {
+    if (dev_err) {
         set_last_error("device error flag " + std::to_string(dev_err));
         return ACB_ERR_DEVICE;
     }
-    return st;
+    return ACB_OK;
+}
+
+acb_dit::~acb_dit() {
+    cudaSetDevice(device);
+    job.reset();
+    drop_graphs();
+    if (st) {
+        cudaStreamDestroy(st);
+    }
+}
+
+namespace {
+
+acb_status run_schedule(DiTRun & r, const GenArgs & g) {
+    for (int k = 0; k < g.num_steps; k++) {
+        const bool last = k == g.num_steps - 1;
+        ACB_TRY(r.step(k, g.schedule[k], last ? 0.0f : g.schedule[k + 1], last, nullptr));
+    }
+    return ACB_OK;
+}
+
+acb_status generate_impl(acb_dit * m, const GenArgs & g) {
+    if (!m || !g.schedule || !g.output || g.num_steps <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    DiTRun r;
+    ACB_TRY(r.begin(m, nullptr, g, 0, g.N, -1, -1));
+    const acb_status st = run_schedule(r, g);
+    if (st != ACB_OK) {
+        cudaStreamSynchronize(m->st);
+        return st;
+    }
+    return r.finish(g.output, false);
 }
 
 }  // namespace
@@ -1205,6 +1360,147 @@ extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, cons
     g.randn_data        = randn_data;
     g.gpu_ms            = gpu_ms;
     return generate_impl(m, g);
+}
+
+// ---- sharded jobs (one process per GPU) ------------------------------------------------------
+
+extern "C" acb_status acb_dit_shard_plan(int n_tracks, int cfg, int world, int rank, int * track0, int * n_local,
+                                         int * half, int * peer) {
+    if (n_tracks <= 0 || world <= 0 || rank < 0 || rank >= world || !track0 || !n_local || !half || !peer) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (n_tracks % world == 0) {
+        // whole track pairs: no exchange during the steps
+        *n_local = n_tracks / world;
+        *track0  = rank * *n_local;
+        *half    = -1;
+        *peer    = -1;
+        return ACB_OK;
+    }
+    if (cfg && world == 2 * n_tracks) {
+        // one CFG half per rank: ranks 2t (conditional) and 2t + 1 (unconditional) share track t
+        *n_local = 1;
+        *track0  = rank / 2;
+        *half    = rank % 2;
+        *peer    = rank ^ 1;
+        return ACB_OK;
+    }
+    set_last_error("acb_dit_shard_plan: " + std::to_string(n_tracks) + " tracks do not shard over " +
+                   std::to_string(world) + " ranks (a divisor of the track count, or two ranks per track with CFG)");
+    return ACB_ERR_UNSUPPORTED;
+}
+
+namespace {
+
+int solver_id(const char * name, acb_status * st) {
+    *st = ACB_OK;
+    if (name && std::strcmp(name, "dpm3m") == 0) {
+        return ACB_SOLVER_DPM3M;
+    }
+    if (name && std::strcmp(name, "sde") == 0) {
+        return ACB_SOLVER_SDE;
+    }
+    if (name && std::strcmp(name, "stork4") == 0) {
+        set_last_error("the STORK4 solver is not provided by this library");
+        *st = ACB_ERR_UNSUPPORTED;
+    }
+    return ACB_SOLVER_EULER;  // solver_lookup's fallback for unknown names
+}
+
+}  // namespace
+
+extern "C" acb_status acb_dit_job_begin(acb_dit * m, acb_comm * comm, const float * noise, const float * context_latents,
+                                        const float * enc_hidden, int enc_S, int T, int N, float guidance_scale,
+                                        const float * context_switch, int cover_steps, acb_cancel_fn cancel,
+                                        void * cancel_data, const int * real_S, const int * real_enc_S,
+                                        const float * enc_switch, const int * real_enc_S_switch,
+                                        const int64_t * seeds, const char * solver_name, acb_randn_fn randn,
+                                        void * randn_data) {
+    if (!m) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    acb_status st     = ACB_OK;
+    const int  solver = solver_id(solver_name, &st);
+    ACB_TRY(st);
+    int t0 = 0, nl = N, half = -1, peer = -1;
+    if (comm) {
+        const bool cfg = guidance_scale > 1.0f && m->null_emb;
+        ACB_TRY(acb_dit_shard_plan(N, cfg ? 1 : 0, comm_world(comm), comm_rank(comm), &t0, &nl, &half, &peer));
+    }
+    GenArgs g;
+    g.noise             = noise;
+    g.context           = context_latents;
+    g.enc               = enc_hidden;
+    g.enc_S             = enc_S;
+    g.T                 = T;
+    g.N                 = N;
+    g.guidance          = guidance_scale;
+    g.context_switch    = context_switch;
+    g.cover_steps       = cover_steps;
+    g.cancel            = cancel;
+    g.cancel_data       = cancel_data;
+    g.real_S            = real_S;
+    g.real_enc_S        = real_enc_S;
+    g.enc_switch        = enc_switch;
+    g.real_enc_S_switch = real_enc_S_switch;
+    g.seeds             = seeds;
+    g.solver            = solver;
+    g.randn             = randn;
+    g.randn_data        = randn_data;
+    m->job.reset(new DiTRun());
+    const acb_status b = m->job->begin(m, comm, g, t0, nl, half, peer);
+    if (b != ACB_OK) {
+        m->job.reset();
+    }
+    return b;
+}
+
+extern "C" acb_status acb_dit_job_step(acb_dit * m, int step, float t_curr, float t_next, int last, float * host_out) {
+    if (!m || !m->job || step < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    return m->job->step(step, t_curr, t_next, last != 0, host_out);
+}
+
+extern "C" acb_status acb_dit_job_end(acb_dit * m, float * output, float * gpu_ms) {
+    if (!m || !m->job || !output) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    m->job->g.gpu_ms      = gpu_ms;
+    const acb_status st   = m->job->finish(output, m->job->comm != nullptr);
+    m->job.reset();
+    return st;
+}
+
+extern "C" acb_stream_t acb_dit_stream(const acb_dit * m) {
+    return m ? (acb_stream_t) m->st : nullptr;
+}
+
+extern "C" acb_status acb_dit_generate_sharded(acb_dit * m, acb_comm * comm, const float * noise,
+                                               const float * context_latents, const float * enc_hidden, int enc_S,
+                                               int T, int N, int num_steps, const float * schedule, float * output,
+                                               float guidance_scale, const float * context_switch, int cover_steps,
+                                               acb_cancel_fn cancel, void * cancel_data, const int * real_S,
+                                               const int * real_enc_S, const float * enc_switch,
+                                               const int * real_enc_S_switch, const int64_t * seeds,
+                                               const char * solver_name, acb_randn_fn randn, void * randn_data,
+                                               float * gpu_ms) {
+    if (!m || !comm || !schedule || !output || num_steps <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    ACB_TRY(acb_dit_job_begin(m, comm, noise, context_latents, enc_hidden, enc_S, T, N, guidance_scale, context_switch,
+                              cover_steps, cancel, cancel_data, real_S, real_enc_S, enc_switch, real_enc_S_switch,
+                              seeds, solver_name, randn, randn_data));
+    GenArgs g       = m->job->g;
+    g.num_steps     = num_steps;
+    g.schedule      = schedule;
+    const acb_status st = run_schedule(*m->job, g);
+    if (st != ACB_OK) {
+        cudaStreamSynchronize(m->st);
+        m->job.reset();
+        return st;
+    }
+    return acb_dit_job_end(m, output, gpu_ms);
 }
 
 extern "C" int acb_dit_eval_kernels(const acb_dit * m) {

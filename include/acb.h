@@ -48,6 +48,7 @@ typedef enum {
     ACB_ERR_FORMAT       = 7, /* malformed or truncated GGUF, missing tensor */
     ACB_ERR_DEVICE       = 8, /* a kernel reported an error through its device flag */
     ACB_ERR_CANCELLED    = 9, /* the caller's cancel callback asked to stop (the reference returns -1) */
+    ACB_ERR_TIMEOUT      = 10, /* a bounded wait on peer GPUs gave up (the communicator is aborted) */
 } acb_status;
 
 typedef enum {

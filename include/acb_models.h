@@ -201,6 +201,55 @@ ACB_API acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, const f
                                        acb_randn_fn randn, void * randn_data, float * gpu_ms);
 ACB_API void       acb_dit_free(acb_dit * m);
 
+/* ---- several GPUs (one process per GPU) ------------------------------------------------------
+ * The reference runs one GPU per process (ace-server pins workers with CUDA_VISIBLE_DEVICES,
+ * tools/ace-server.cpp:2095-2120) and has no collectives. These entry points let a C/C++ host shard
+ * one DiT job over the GPUs of a node: every rank holds a full copy of the weights and evaluates
+ * its own sequences; NCCL (libnccl.so.2, opened at run time) moves the per-step velocity between
+ * the two ranks of a split CFG pair and gathers the finished latents. Every wait on peers is
+ * bounded by the communicator's timeout: on expiry the communicator is aborted and the call
+ * returns ACB_ERR_TIMEOUT. */
+typedef struct acb_comm acb_comm;
+/* 128-byte NCCL unique id, made on one rank and handed to the others by the host's own channel. */
+ACB_API acb_status acb_comm_unique_id(void * id128);
+ACB_API acb_status acb_comm_init(const void * id128, int world, int rank, int device, int timeout_ms, acb_comm ** out);
+ACB_API int        acb_comm_rank(const acb_comm * c);
+ACB_API int        acb_comm_world(const acb_comm * c);
+ACB_API void       acb_comm_free(acb_comm * c);
+
+/* Which tracks rank `rank` of `world` evaluates in a job of n_tracks (host logic only): when world
+ * divides n_tracks, the whole track pairs [track0, track0 + n_local) (half = -1, no exchange during
+ * the steps); with CFG and world == 2 * n_tracks, one half of track rank / 2 (half 0 conditional,
+ * 1 unconditional) whose other half is on rank `peer` (one velocity exchange per step). Otherwise
+ * ACB_ERR_UNSUPPORTED. */
+ACB_API acb_status acb_dit_shard_plan(int n_tracks, int cfg, int world, int rank, int * track0, int * n_local,
+                                      int * half, int * peer);
+/* dit_ggml_generate sharded over the communicator's ranks. Every rank passes the whole job's host
+ * arrays (as acb_dit_generate_ex) and receives every track's x0 in output [N][T][out_channels]. */
+ACB_API acb_status acb_dit_generate_sharded(acb_dit * m, acb_comm * comm, const float * noise,
+                                            const float * context_latents, const float * enc_hidden, int enc_S, int T,
+                                            int N, int num_steps, const float * schedule, float * output,
+                                            float guidance_scale, const float * context_switch, int cover_steps,
+                                            acb_cancel_fn cancel, void * cancel_data, const int * real_S,
+                                            const int * real_enc_S, const float * enc_switch,
+                                            const int * real_enc_S_switch, const int64_t * seeds,
+                                            const char * solver_name, acb_randn_fn randn, void * randn_data,
+                                            float * gpu_ms);
+/* The same job one step at a time, for hosts that drive the schedule themselves: begin (comm may be
+ * NULL: the whole job on this GPU), then step k with (t_curr, t_next) -- last != 0 for the final
+ * x0 step; host_out (optional) receives this rank's xt after the step, or x0 after the last --,
+ * then end (output: every track's x0; gpu_ms: device time from the first step). Steps run on
+ * acb_dit_stream(m). */
+ACB_API acb_status   acb_dit_job_begin(acb_dit * m, acb_comm * comm, const float * noise, const float * context_latents,
+                                       const float * enc_hidden, int enc_S, int T, int N, float guidance_scale,
+                                       const float * context_switch, int cover_steps, acb_cancel_fn cancel,
+                                       void * cancel_data, const int * real_S, const int * real_enc_S,
+                                       const float * enc_switch, const int * real_enc_S_switch, const int64_t * seeds,
+                                       const char * solver_name, acb_randn_fn randn, void * randn_data);
+ACB_API acb_status   acb_dit_job_step(acb_dit * m, int step, float t_curr, float t_next, int last, float * host_out);
+ACB_API acb_status   acb_dit_job_end(acb_dit * m, float * output, float * gpu_ms);
+ACB_API acb_stream_t acb_dit_stream(const acb_dit * m);
+
 /* ---- Qwen3 causal LM (replaces src/qwen3-lm.h) ---------------------------------------------- */
 
 typedef struct acb_qw3lm acb_qw3lm;
