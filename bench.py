@@ -434,6 +434,42 @@ def run_ours(args):
     if args.workloads == "gemv":
         print(json.dumps(run_gemv_shapes(dev)), flush=True)
         return
+    if args.workloads == "dit1":
+        # profiling target: the per-GPU evaluation of config 4 at 8 GPUs (one 750-token sequence)
+        import tempfile
+
+        import numpy as np
+
+        import synthetic
+        cfg = dict(synthetic.ACESTEP_DIT_2B)
+        path = os.path.join(tempfile.gettempdir(), "acb_bench_dit1.gguf")
+        synthetic.write_dit_gguf(path, cfg, synthetic.Q8_0, seed=21, device=str(dev))
+        dit = acb.DiT(path, device=dev.index or 0)
+        os.remove(path)
+        rng = np.random.default_rng(3)
+        n_seq = int(os.environ.get("ACB_DIT1_SEQ", "1"))
+        x = torch.from_numpy(rng.standard_normal((n_seq, DIT_T, cfg["in_channels"])).astype(np.float32)).to(dev)
+        e = torch.from_numpy(rng.standard_normal((n_seq, DIT_ENC_S, cfg["enc_hidden_size"])).astype(np.float32)).to(dev)
+        out = torch.empty((n_seq, DIT_T, cfg["out_channels"]), device=dev)
+        tt = torch.tensor([0.8, 0.8], device=dev)
+        dit.set_condition(e, DIT_T)
+        for _ in range(3):
+            dit.eval(x, tt, out)
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(10):
+            dit.eval(x, tt, out)
+        ev1.record()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        dit.eval(x, tt, out)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        print(json.dumps({"workload": "dit1", "sequences": n_seq, "ms_per_eval": ev0.elapsed_time(ev1) / 10,
+                          "kernels_per_eval": dit.eval_kernels()}), flush=True)
+        dit.close()
+        return
     if args.workloads == "gemm_exact":
         # profiling target: three launches of the DiT's dominant kernel (exact gate|up), nothing else
         import torch as _t
