@@ -148,6 +148,28 @@ def lib():
             "acb_gemm_qkv_planes": (I, [P, I64, P, I64, I64, I64, I, I, P, P, F, P, P, I, I64, P, I64, I64, P, I64, I64,
                                         I, P, P]),
             "acb_gemm_pair_clusters": (I, [I]),
+            "acb_fsq_project_out": (I, [P, I, P, I, I, P, P, I64, P, P]),
+            "acb_fsq_quantize": (I, [P, I64, P, I, P, P]),
+            "acb_rows_repeat_add": (I, [P, I64, P, I64, I, I, I, P, I64, P]),
+            "acb_rows_prepend": (I, [P, P, I64, I, I, I, P, I64, P]),
+            "acb_fsq_decode_index": (None, [I, P]),
+            "acb_fsq_encode_index": (I, [P]),
+            "acb_cond_load": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
+            "acb_cond_set_exact": (I, [P, I]),
+            "acb_cond_forward": (I, [P, P, I, P, I, P, I, P, P]),
+            "acb_cond_forward_device": (I, [P, P, I, P, I, P, I, P, P, P]),
+            "acb_cond_null_embedding": (I, [P, P]),
+            "acb_cond_free": (None, [P]),
+            "acb_detok_load": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
+            "acb_detok_set_exact": (I, [P, I]),
+            "acb_detok_decode": (I, [P, P, I, P]),
+            "acb_detok_decode_device": (I, [P, P, I, P, P]),
+            "acb_detok_free": (None, [P]),
+            "acb_tok_load": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
+            "acb_tok_set_exact": (I, [P, I]),
+            "acb_tok_encode": (I, [P, P, I, P, P, P]),
+            "acb_tok_encode_device": (I, [P, P, I, P, P]),
+            "acb_tok_free": (None, [P]),
             "acb_gemm_tc": (I, [P, I64, P, I64, I64, I64, I64, P, I, I64, P, P, I64, P, I64, I64, I, P, C.c_size_t, P,
                                 P]),
         }
@@ -606,6 +628,157 @@ class Qwen3Encoder:
         _check("acb_qwen3_embed_lookup", lib().acb_qwen3_embed_lookup(self.h, ids.ctypes.data, ids.size,
                                                                       out.ctypes.data))
         return out
+
+
+def fsq_decode_index(index: int):
+    """fsq_decode_index (src/fsq-detok.h:18-29): flat code -> 6 floats in [-1, 1]."""
+    import numpy as np
+    out = np.empty(6, dtype=np.float32)
+    lib().acb_fsq_decode_index(int(index), out.ctypes.data)
+    return out
+
+
+def fsq_encode_index(raw6) -> int:
+    """fsq_encode_index (src/fsq-tok.h:42-60): 6 project_in outputs -> flat code."""
+    import numpy as np
+    r = np.ascontiguousarray(raw6, dtype=np.float32)
+    return int(lib().acb_fsq_encode_index(r.ctypes.data))
+
+
+def _load_handle(fn: str, path: str, device: int):
+    h = C.c_void_p()
+    st = getattr(lib(), fn)(path.encode(), device, C.byref(h))
+    if st != 0:
+        raise AcbError(f"{fn} ({lib().acb_last_error().decode()})", st)
+    return h
+
+
+class CondEncoder:
+    """Condition encoder (acb_models.h): cond_ggml_load / cond_ggml_forward of src/cond-enc.h."""
+
+    FIELDS = ["hidden_size", "text_dim", "lyric_dim", "timbre_dim", "lyric_layers", "timbre_layers", "window",
+              "timbre_cls"]
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        self.h = _load_handle("acb_cond_load", gguf_path, device)
+
+        class Cfg(C.Structure):
+            _fields_ = [(f, C.c_int) for f in CondEncoder.FIELDS]
+        c = Cfg()
+        fn = lib().acb_cond_get_config
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.POINTER(Cfg)]
+        _check("acb_cond_get_config", fn(self.h, C.byref(c)))
+        self.cfg = {f: getattr(c, f) for f in CondEncoder.FIELDS}
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().acb_cond_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_exact(self, exact: bool):
+        _check("acb_cond_set_exact", lib().acb_cond_set_exact(self.h, int(bool(exact))))
+
+    def forward(self, text_hidden, lyric_embed, timbre_feats=None):
+        """Host f32 [S_text][text_dim], [S_lyric][lyric_dim], [S_ref][timbre_dim] or None ->
+        packed encoder states [S_lyric + (1) + S_text][hidden_size]."""
+        import numpy as np
+        t = np.ascontiguousarray(text_hidden, dtype=np.float32)
+        ly = np.ascontiguousarray(lyric_embed, dtype=np.float32)
+        tb = None if timbre_feats is None else np.ascontiguousarray(timbre_feats, dtype=np.float32)
+        S_ref = 0 if tb is None else tb.shape[0]
+        S = ly.shape[0] + (1 if S_ref > 0 else 0) + t.shape[0]
+        out = np.empty((S, self.cfg["hidden_size"]), dtype=np.float32)
+        n = C.c_int(0)
+        _check("acb_cond_forward", lib().acb_cond_forward(
+            self.h, t.ctypes.data, t.shape[0], ly.ctypes.data, ly.shape[0], None if tb is None else tb.ctypes.data,
+            S_ref, out.ctypes.data, C.byref(n)))
+        assert n.value == S
+        return out
+
+    def forward_device(self, text_hidden, lyric_embed, timbre_feats, out, stream=None):
+        """Device tensors in, packed states into device `out`; returns the row count."""
+        n = C.c_int(0)
+        S_ref = 0 if timbre_feats is None else timbre_feats.shape[0]
+        _check("acb_cond_forward_device", lib().acb_cond_forward_device(
+            self.h, _ptr(text_hidden), text_hidden.shape[0], _ptr(lyric_embed), lyric_embed.shape[0],
+            None if timbre_feats is None else _ptr(timbre_feats), S_ref, _ptr(out), C.byref(n), _stream(stream)))
+        return n.value
+
+    def null_embedding(self):
+        import numpy as np
+        out = np.empty(self.cfg["hidden_size"], dtype=np.float32)
+        _check("acb_cond_null_embedding", lib().acb_cond_null_embedding(self.h, out.ctypes.data))
+        return out
+
+
+class Detokenizer:
+    """FSQ detokenizer (acb_models.h): detok_ggml_load / detok_ggml_decode of src/fsq-detok.h."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        self.h = _load_handle("acb_detok_load", gguf_path, device)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().acb_detok_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_exact(self, exact: bool):
+        _check("acb_detok_set_exact", lib().acb_detok_set_exact(self.h, int(bool(exact))))
+
+    def decode(self, codes, channels: int = 64):
+        """Host codes [T_5Hz] -> host context latents [T_5Hz * 5][channels]."""
+        import numpy as np
+        c = np.ascontiguousarray(codes, dtype=np.int32)
+        out = np.empty((c.size * 5, channels), dtype=np.float32)
+        _check("acb_detok_decode", lib().acb_detok_decode(self.h, c.ctypes.data, c.size, out.ctypes.data))
+        return out
+
+    def decode_device(self, codes, out, stream=None):
+        _check("acb_detok_decode_device", lib().acb_detok_decode_device(self.h, _ptr(codes), codes.numel(),
+                                                                        _ptr(out), _stream(stream)))
+        return out
+
+
+class Tokenizer:
+    """FSQ tokenizer (acb_models.h): tok_ggml_load / tok_ggml_encode of src/fsq-tok.h."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        self.h = _load_handle("acb_tok_load", gguf_path, device)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().acb_tok_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_exact(self, exact: bool):
+        _check("acb_tok_set_exact", lib().acb_tok_set_exact(self.h, int(bool(exact))))
+
+    def encode(self, latents, silence_latent=None):
+        """Host latents [T_25Hz][64] (padded to a multiple of 5 from silence_latent) -> codes [T_5Hz]."""
+        import numpy as np
+        x = np.ascontiguousarray(latents, dtype=np.float32)
+        sl = None if silence_latent is None else np.ascontiguousarray(silence_latent, dtype=np.float32)
+        codes = np.empty((x.shape[0] + 4) // 5, dtype=np.int32)
+        n = C.c_int(0)
+        _check("acb_tok_encode", lib().acb_tok_encode(self.h, x.ctypes.data, x.shape[0], codes.ctypes.data,
+                                                      None if sl is None else sl.ctypes.data, C.byref(n)))
+        assert n.value == codes.size
+        return codes
+
+    def encode_device(self, latents, codes, stream=None):
+        """Device f32 latents [5 * T_5Hz][64] -> device int32 codes [T_5Hz]."""
+        _check("acb_tok_encode_device", lib().acb_tok_encode_device(self.h, _ptr(latents), codes.numel(),
+                                                                    _ptr(codes), _stream(stream)))
+        return codes
 
 
 LAYOUT_PLAIN, LAYOUT_GEMM_A, LAYOUT_GEMM_B, LAYOUT_PLANES = 0, 1, 2, 3

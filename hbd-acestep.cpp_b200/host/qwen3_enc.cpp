@@ -28,6 +28,7 @@
 
 #include "../../include/acb_models.h"
 #include "dense.h"
+#include "enc_stack.h"
 #include "gguf.h"
 #include "host_common.h"
 #include "weights.h"
@@ -48,6 +49,7 @@ constexpr int kPdl = ACB_FLAG_PDL;
 struct acb_qwen3_enc {
     int                   device = 0;
     acb_qwen3_config      c{};
+    int                   window = 0;  // non-causal stacks: |i - j| <= window on even layers (cond-enc.h:203-208)
     WeightArena           arena;  // embedding table (GGUF type) and F32 norms
     DevBuf                w16;    // every linear, 16-bit
     DevTensor *           embed = nullptr, *final_norm = nullptr;
@@ -55,10 +57,10 @@ struct acb_qwen3_enc {
     cudaStream_t          st    = nullptr;
     bool                  exact = true;
 
-    // scratch for up to cap tokens
-    int                            cap = 0;
+    // scratch for up to cap rows; positions restart every `period` rows (0: row index)
+    int                            cap = 0, period = 0;
     DevBuf                         ids, pos, rope, h, xn, xq, qkv, qkv32, planes, vtb, q, k, att, gu, out, err, ws;
-    int                            s_ld = 0;  // V^T row length: cap rounded up to 8
+    int                            s_ld = 0;  // V^T row length: the sequence length rounded up to 8
     std::map<int, cudaGraphExec_t> graphs;  // one per S * 2 + exact
 
     ~acb_qwen3_enc() {
@@ -78,21 +80,49 @@ struct acb_qwen3_enc {
 
     int nqkv() const { return (c.n_heads + 2 * c.n_kv_heads) * c.head_dim; }
 
-    acb_status reserve(int S);
+    // room for R rows in sequences of S rows; period: S for a batch of sequences, 0 for one
+    acb_status reserve(int R, int S, int period);
+    acb_status reserve(int S) { return reserve(S, S, 0); }
     DenseScratch scratch() { return DenseScratch{ xq.p, ws.p, ws.bytes, err.as<int>() }; }
-    acb_status enqueue_layers(int S, int l0, int l1, cudaStream_t s);
+    // layers [l0, l1) over B sequences of S rows in h (positions 0..S-1 in each)
+    acb_status enqueue_layers(int B, int S, int l0, int l1, cudaStream_t s);
+    acb_status enqueue_layers(int S, int l0, int l1, cudaStream_t s) { return enqueue_layers(1, S, l0, l1, s); }
     acb_status enqueue(int S, cudaStream_t s);
     acb_status run(int S, cudaStream_t s);
 };
 
-acb_status acb_qwen3_enc::reserve(int S) {
-    if (S <= cap) {
+acb_status acb_qwen3_enc::reserve(int R, int S, int per) {
+    const size_t KD = (size_t) c.n_kv_heads * c.head_dim;
+    if (R <= cap) {
+        // V^T of ceil(cap / S) sequences of round8(S) columns, hi and lo planes
+        const int    ld   = (S + 7) / 8 * 8;
+        const size_t vneed = (size_t) 2 * KD * ld * 2 * ((cap + S - 1) / S);
+        if (vneed > vtb.bytes) {
+            drop_graphs();
+            if (vtb.alloc(vneed) != ACB_OK) {
+                cap = 0;
+                set_last_error("encoder scratch allocation failed");
+                return ACB_ERR_OOM;
+            }
+        }
+        s_ld = ld;
+        if (per != period) {
+            // the positions of a captured graph (one sequence: rows 0..S-1) do not depend on the period
+            std::vector<int32_t> p((size_t) cap);
+            for (int i = 0; i < cap; i++) {
+                p[(size_t) i] = per > 0 ? i % per : i;
+            }
+            if (cudaMemcpy(pos.p, p.data(), p.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+                return ACB_ERR_CUDA;
+            }
+            period = per;
+        }
         return ACB_OK;
     }
     drop_graphs();
-    const int    n  = std::max(S, 256);
+    const int    n  = std::max({ R, cap, 256 });
     const size_t H  = (size_t) c.hidden_size, F = (size_t) c.intermediate_size;
-    const size_t QD = (size_t) c.n_heads * c.head_dim, KD = (size_t) c.n_kv_heads * c.head_dim;
+    const size_t QD = (size_t) c.n_heads * c.head_dim;
     const size_t XQ = std::max({ H, QD, F });
     bool         bad = false;
     bad |= ids.alloc((size_t) n * 4) != ACB_OK;
@@ -103,8 +133,8 @@ acb_status acb_qwen3_enc::reserve(int S) {
     bad |= qkv.alloc((size_t) n * nqkv() * 2) != ACB_OK;
     bad |= qkv32.alloc((size_t) n * nqkv() * 4) != ACB_OK;
     bad |= planes.alloc((size_t) n * (QD + KD) * 2 * 2) != ACB_OK;
-    s_ld = (n + 7) / 8 * 8;
-    bad |= vtb.alloc((size_t) 2 * KD * s_ld * 2) != ACB_OK;
+    s_ld = (S + 7) / 8 * 8;
+    bad |= vtb.alloc((size_t) 2 * KD * s_ld * 2 * ((n + S - 1) / S)) != ACB_OK;
     bad |= q.alloc((size_t) n * QD * 2) != ACB_OK;
     bad |= k.alloc((size_t) n * KD * 2) != ACB_OK;
     bad |= att.alloc((size_t) n * QD * 4) != ACB_OK;
@@ -134,7 +164,7 @@ acb_status acb_qwen3_enc::reserve(int S) {
     }
     std::vector<int32_t> p((size_t) n);
     for (int i = 0; i < n; i++) {
-        p[(size_t) i] = i;  // positions 0..S-1 (qwen3-enc.h:418-424)
+        p[(size_t) i] = per > 0 ? i % per : i;  // positions 0..S-1 of every sequence (qwen3-enc.h:418-424)
     }
     std::vector<float> tab((size_t) n * c.head_dim);
     acb_rope_table_host(tab.data(), n, c.head_dim, c.rope_theta);
@@ -142,12 +172,14 @@ acb_status acb_qwen3_enc::reserve(int S) {
         cudaMemcpy(rope.p, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
-    cap = n;
+    cap    = n;
+    period = per;
     return ACB_OK;
 }
 
-// Layers [l0, l1) over the hidden states in `h` (qwen3_build_layers, qwen3-enc.h:249-262).
-acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) {
+// Layers [l0, l1) over the hidden states in `h` (qwen3_build_layers, qwen3-enc.h:249-262): B
+// sequences of S rows each, attention within each sequence.
+acb_status acb_qwen3_enc::enqueue_layers(int B, int S, int l0, int l1, cudaStream_t s) {
     const int          H = c.hidden_size, Nh = c.n_heads, Nkv = c.n_kv_heads, D = c.head_dim;
     const int          QD = Nh * D, KD = Nkv * D, NQKV = nqkv();
     const float        eps   = c.rms_norm_eps;
@@ -156,9 +188,11 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
     const DenseScratch sc    = scratch();
     int *              e     = err.as<int>();
     float *            hp    = h.as<float>();
-    const int          mask  = c.is_causal ? 1 : 0;
+    const int          R     = B * S;
     for (int l = l0; l < l1; l++) {
         const EncLayer & L = layers[(size_t) l];
+        // causal (text encoder), or bidirectional with the sliding window on even layers
+        const int mask = c.is_causal ? 1 : ((window > 0 && l % 2 == 0 && S > window + 1) ? 2 : 0);
         // attention output straight into the output projection's operand when possible
         int        ao_type = ACB_TYPE_F32, ao_flags = 0;
         int64_t    ao_ts   = QD;
@@ -175,61 +209,61 @@ acb_status acb_qwen3_enc::enqueue_layers(int S, int l0, int l1, cudaStream_t s) 
         NormSpec ns_in;
         ns_in.w   = (const float *) L.attn_norm->data;
         ns_in.eps = eps;
-        if (Nh % 2 == 0 && Nkv % 2 == 0 && S >= kQkvFuseMinRows) {
+        if (Nh % 2 == 0 && Nkv % 2 == 0 && R >= kQkvFuseMinRows) {
             // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue
             const int64_t W  = QD + KD;
             const int64_t lo = exact ? (int64_t) cap * W : 0;
-            const int64_t vl = exact ? (int64_t) KD * s_ld : 0;
+            const int64_t vl = exact ? (int64_t) B * KD * s_ld : 0;
             uint16_t *    hi = planes.as<uint16_t>();
             int64_t       Kp = 0;
-            ACB_TRY(dense_operand(L.qkv, exact, hp, H, S, sc, s, &ns_in, &Kp));
-            ACB_TRY(acb_gemm_qkv_planes(sc.xq, Kp, L.qkv.w, L.qkv.ldw, S, Kp, Nh, Nkv, (const float *) L.q_norm->data,
+            ACB_TRY(dense_operand(L.qkv, exact, hp, H, R, sc, s, &ns_in, &Kp));
+            ACB_TRY(acb_gemm_qkv_planes(sc.xq, Kp, L.qkv.w, L.qkv.ldw, R, Kp, Nh, Nkv, (const float *) L.q_norm->data,
                                         (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap,
                                         S, hi, W, lo, vtb.as<uint16_t>(), s_ld, vl, kPdl | L.qkv.op, e, as));
-            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, B, S, S, Nh, Nkv, D, mask, window, 0,
                                 scale, kPdl | ao_flags, lo, lo, vl, e, as));
         } else if (exact) {
             float * q32 = qkv32.as<float>();
-            ACB_TRY(dense_forward(L.qkv, true, hp, H, 0, S, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0,
+            ACB_TRY(dense_forward(L.qkv, true, hp, H, 0, R, q32, ACB_TYPE_F32, NQKV, nullptr, nullptr, 0, nullptr, 0,
                                   0, sc, s, &ns_in));
             // q/k norm + rope straight into hi/lo planes of Q||K, and V^T planes, for the
             // tensor-core attention
             const int64_t W  = QD + KD;
             const int64_t lo = (int64_t) cap * W;
-            const int64_t vl = (int64_t) KD * s_ld;
+            const int64_t vl = (int64_t) B * KD * s_ld;
             uint16_t *    hi = planes.as<uint16_t>();
-            ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, S, Nh, (const float *) L.q_norm->data,
+            ACB_TRY(acb_qk_norm_rope_planes(q32, ACB_TYPE_F32, NQKV, hi, W, lo, R, Nh, (const float *) L.q_norm->data,
                                             Nkv, (const float *) L.k_norm->data, D, eps, pos.as<int32_t>(),
                                             rope.as<float>(), cap, e, as));
-            ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D, vtb.p, s_ld, vl,
+            ACB_TRY(acb_attn_vt(q32 + QD + KD, ACB_TYPE_F32, (int64_t) S * NQKV, NQKV, B, S, Nkv, D, vtb.p, s_ld, vl,
                                 as));
-            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+            ACB_TRY(acb_attn_tc(hi, W, hi + QD, W, vtb.p, s_ld, ao, ao_type, ao_ts, B, S, S, Nh, Nkv, D, mask, window, 0,
                                 scale, kPdl | ao_flags, lo, lo, vl, e, as));
         } else {
-            ACB_TRY(dense_forward(L.qkv, false, hp, H, 0, S, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
+            ACB_TRY(dense_forward(L.qkv, false, hp, H, 0, R, qkv.p, ACB_TYPE_F16, NQKV, nullptr, nullptr, 0, nullptr, 0,
                                   0, sc, s, &ns_in));
-            ACB_TRY(acb_qk_norm_rope(qkv.p, ACB_TYPE_F16, NQKV, q.p, ACB_TYPE_F16, QD, D, 0, S, Nh, D,
+            ACB_TRY(acb_qk_norm_rope(qkv.p, ACB_TYPE_F16, NQKV, q.p, ACB_TYPE_F16, QD, D, 0, R, Nh, D,
                                      (const float *) L.q_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap, e,
                                      as));
-            ACB_TRY(acb_qk_norm_rope(qkv.as<uint16_t>() + QD, ACB_TYPE_F16, NQKV, k.p, ACB_TYPE_F16, KD, D, 0, S, Nkv,
+            ACB_TRY(acb_qk_norm_rope(qkv.as<uint16_t>() + QD, ACB_TYPE_F16, NQKV, k.p, ACB_TYPE_F16, KD, D, 0, R, Nkv,
                                      D, (const float *) L.k_norm->data, eps, pos.as<int32_t>(), rope.as<float>(), cap,
                                      e, as));
-            ACB_TRY(acb_attn_vt(qkv.as<uint16_t>() + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, 1, S, Nkv, D,
+            ACB_TRY(acb_attn_vt(qkv.as<uint16_t>() + QD + KD, ACB_TYPE_F16, (int64_t) S * NQKV, NQKV, B, S, Nkv, D,
                                 vtb.p, s_ld, 0, as));
-            ACB_TRY(acb_attn_tc(q.p, QD, k.p, KD, vtb.p, s_ld, ao, ao_type, ao_ts, 1, S, S, Nh, Nkv, D, mask, 0, 0,
+            ACB_TRY(acb_attn_tc(q.p, QD, k.p, KD, vtb.p, s_ld, ao, ao_type, ao_ts, B, S, S, Nh, Nkv, D, mask, window, 0,
                                 scale, kPdl | ao_flags, 0, 0, 0, e, as));
         }
         if (fuse_o) {  // the attention wrote the output projection's operand
-            ACB_TRY(dense_forward_operand(L.o, exact, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0, sc, s));
+            ACB_TRY(dense_forward_operand(L.o, exact, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0, 0, sc, s));
         } else {
-            ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, S, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
+            ACB_TRY(dense_forward(L.o, exact, att.as<float>(), QD, 0, R, hp, ACB_TYPE_F32, H, nullptr, hp, H, nullptr, 0,
                                   0, sc, s));
         }
         // post_attention_layernorm inside the gate/up projection's producer
         NormSpec ns_post;
         ns_post.w   = (const float *) L.post_norm->data;
         ns_post.eps = eps;
-        ACB_TRY(dense_ffn(L.gu, L.down, exact, hp, H, S, hp, H, hp, H, nullptr, 0, 0, gu.p, sc, s, &ns_post));
+        ACB_TRY(dense_ffn(L.gu, L.down, exact, hp, H, R, hp, H, hp, H, nullptr, 0, 0, gu.p, sc, s, &ns_post));
     }
     return ACB_OK;
 }
@@ -277,35 +311,24 @@ acb_status acb_qwen3_enc::run(int S, cudaStream_t s) {
 
 // ---- C ABI ---------------------------------------------------------------------------------------
 
-extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int device, acb_qwen3_enc ** out) {
-    if (!gguf_path || !out) {
-        return ACB_ERR_INVALID_ARG;
-    }
+namespace acb {
+
+// A Qwen3 layer stack whose tensors are `prefix`layers.{i}.* and `prefix`norm.weight (with
+// `prefix`embed_tokens.weight when with_embed): the text encoder (prefix "", qwen3-enc.h:319-360) and
+// the stacks of the condition encoder and the FSQ (de)tokenizer (cond-enc.h:97-135,
+// fsq-tok.h:86-112, fsq-detok.h:83-110), which share qwen3_load_layer.
+acb_status enc_stack_load(GGUFFile & gf, const std::string & prefix, const acb_qwen3_config & cfg, int window,
+                          bool with_embed, int device, acb_qwen3_enc ** out) {
     *out = nullptr;
     if (cudaSetDevice(device) != cudaSuccess) {
         set_last_error("cannot select CUDA device");
         return ACB_ERR_CUDA;
     }
-    GGUFFile gf;
-    if (!gf.open(gguf_path)) {
-        set_last_error(gf.error());
-        return gf.error().rfind("cannot open", 0) == 0 ? ACB_ERR_IO : ACB_ERR_FORMAT;
-    }
     std::unique_ptr<acb_qwen3_enc> m(new acb_qwen3_enc());
     m->device            = device;
+    m->window            = window;
     acb_qwen3_config & c = m->c;
-    c                    = { 1024, 3072, 16, 8, 128, 28, 1000000.0f, 1e-6f, 1, 0 };  // qwen3-enc.h:327-337
-    const char * j       = gf.get_str("acestep.config_json");
-    if (j && j[0]) {
-        c.hidden_size       = json_int(j, "hidden_size", c.hidden_size);
-        c.intermediate_size = json_int(j, "intermediate_size", c.intermediate_size);
-        c.n_heads           = json_int(j, "num_attention_heads", c.n_heads);
-        c.n_kv_heads        = json_int(j, "num_key_value_heads", c.n_kv_heads);
-        c.head_dim          = json_int(j, "head_dim", c.head_dim);
-        c.n_layers          = json_int(j, "num_hidden_layers", c.n_layers);
-        c.rope_theta        = json_float(j, "rope_theta", c.rope_theta);
-        c.rms_norm_eps      = json_float(j, "rms_norm_eps", c.rms_norm_eps);
-    }
+    c                    = cfg;
     auto bad = [&](acb_status s, const std::string & msg) {
         set_last_error(msg);
         return s;
@@ -323,8 +346,8 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
     // once their 16-bit copies exist.
     WeightArena & A     = m->arena;
     auto          stage = std::make_unique<WeightArena>();
-    m->embed            = A.load(gf, "embed_tokens.weight");
-    m->final_norm       = A.load_f32(gf, "norm.weight");
+    m->embed            = with_embed ? A.load(gf, prefix + "embed_tokens.weight") : nullptr;
+    m->final_norm       = A.load_f32(gf, prefix + "norm.weight");
     struct Raw {
         std::vector<DevTensor *> qkv, gu;
         DevTensor *              o = nullptr, *down = nullptr;
@@ -333,7 +356,7 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
     m->layers.resize((size_t) c.n_layers);
     const int QD = c.n_heads * D, KD = c.n_kv_heads * D;
     for (int i = 0; i < c.n_layers; i++) {
-        const std::string p = "layers." + std::to_string(i);
+        const std::string p = prefix + "layers." + std::to_string(i);
         EncLayer &        L = m->layers[(size_t) i];
         Raw &             R = raw[(size_t) i];
         L.attn_norm         = A.load_f32(gf, p + ".input_layernorm.weight");
@@ -362,13 +385,13 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
             return bad(ACB_ERR_FORMAT, "layer tensor shapes do not match the config");
         }
     }
-    if (!m->embed || !m->final_norm) {
-        return bad(ACB_ERR_FORMAT, A.error);
+    if ((with_embed && !m->embed) || !m->final_norm) {
+        return bad(ACB_ERR_FORMAT, A.error.empty() ? "missing embedding or final norm" : A.error);
     }
-    if (m->embed->K != H) {
+    if (m->embed && m->embed->K != H) {
         return bad(ACB_ERR_FORMAT, "embed_tokens shape does not match the config");
     }
-    c.vocab_size = (int) m->embed->N;
+    c.vocab_size = m->embed ? (int) m->embed->N : 0;
     ACB_TRY(A.upload(m->st));
     ACB_TRY(stage->upload(m->st));
 
@@ -421,6 +444,56 @@ extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int de
     ACB_TRY(m->reserve(256));
     *out = m.release();
     return ACB_OK;
+}
+
+float * enc_stack_input(acb_qwen3_enc * m, int B, int S, cudaStream_t s) {
+    if (B <= 0 || S <= 0 || (int64_t) B * S > (1 << 30)) {
+        set_last_error("encoder batch shape out of range");
+        return nullptr;
+    }
+    // the positions are rewritten synchronously: nothing may still read them
+    if (cudaStreamSynchronize(s) != cudaSuccess || cudaStreamSynchronize(m->st) != cudaSuccess) {
+        return nullptr;
+    }
+    return m->reserve(B * S, S, B > 1 ? S : 0) == ACB_OK ? m->h.as<float>() : nullptr;
+}
+
+acb_status enc_stack_run(acb_qwen3_enc * m, int B, int S, float * d_out, int64_t ldo, cudaStream_t s) {
+    ACB_TRY(m->enqueue_layers(B, S, 0, m->c.n_layers, s));
+    const int H = m->c.hidden_size;
+    return acb_rms_norm(m->h.p, ACB_TYPE_F32, H, (const float *) m->final_norm->data, d_out, ACB_TYPE_F32, ldo,
+                        (int64_t) B * S, H, m->c.rms_norm_eps, (acb_stream_t) s);
+}
+
+int * enc_stack_err(acb_qwen3_enc * m) {
+    return m->err.as<int>();
+}
+
+}  // namespace acb
+
+extern "C" acb_status acb_qwen3_load_text_encoder(const char * gguf_path, int device, acb_qwen3_enc ** out) {
+    if (!gguf_path || !out) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    *out = nullptr;
+    GGUFFile gf;
+    if (!gf.open(gguf_path)) {
+        set_last_error(gf.error());
+        return gf.error().rfind("cannot open", 0) == 0 ? ACB_ERR_IO : ACB_ERR_FORMAT;
+    }
+    acb_qwen3_config c = { 1024, 3072, 16, 8, 128, 28, 1000000.0f, 1e-6f, 1, 0 };  // qwen3-enc.h:327-337
+    const char *     j = gf.get_str("acestep.config_json");
+    if (j && j[0]) {
+        c.hidden_size       = json_int(j, "hidden_size", c.hidden_size);
+        c.intermediate_size = json_int(j, "intermediate_size", c.intermediate_size);
+        c.n_heads           = json_int(j, "num_attention_heads", c.n_heads);
+        c.n_kv_heads        = json_int(j, "num_key_value_heads", c.n_kv_heads);
+        c.head_dim          = json_int(j, "head_dim", c.head_dim);
+        c.n_layers          = json_int(j, "num_hidden_layers", c.n_layers);
+        c.rope_theta        = json_float(j, "rope_theta", c.rope_theta);
+        c.rms_norm_eps      = json_float(j, "rms_norm_eps", c.rms_norm_eps);
+    }
+    return enc_stack_load(gf, "", c, 0, true, device, out);
 }
 
 extern "C" acb_status acb_qwen3_set_exact(acb_qwen3_enc * m, int exact) {

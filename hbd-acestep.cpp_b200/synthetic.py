@@ -183,10 +183,95 @@ def dit_tensors(cfg: dict, qtype: int = Q8_0, seed: int = 0, device: str = "cuda
         yield vec("null_condition_emb", (He,), 0.0, 1.0)
 
 
+# Condition encoder and FSQ models (src/cond-enc.h, src/fsq-tok.h, src/fsq-detok.h): the
+# reference's sizes, and a small stand-in for parity tests against the oracle.
+ACESTEP_COND = dict(hidden_size=2048, intermediate_size=6144, n_heads=16, n_kv_heads=8, head_dim=128,
+                    lyric_layers=8, timbre_layers=4, tok_layers=2, detok_layers=2, text_dim=1024, lyric_dim=1024,
+                    latent_dim=64)
+COND_TINY = dict(hidden_size=256, intermediate_size=512, n_heads=4, n_kv_heads=2, head_dim=128, lyric_layers=2,
+                 timbre_layers=2, tok_layers=2, detok_layers=2, text_dim=256, lyric_dim=256, latent_dim=64)
+
+
+def _block_of(qtype: int) -> int:
+    return {Q8_0: 32, Q4_K: 256, Q6_K: 256}.get(qtype, 1)
+
+
+def cond_tensors(ccfg: dict, qtype: int = Q8_0, seed: int = 0, device: str = "cuda", timbre_cls: bool = False):
+    """Yields (name, qtype, raw, K, shape) of the encoder.*, tokenizer.* and detokenizer.* tensors of
+    a DiT GGUF with the quantize tool's choices (tools/quantize.cpp:97-171): 2-D tensors whose
+    innermost size is a block multiple in `qtype` (the detokenizer's special_tokens [1, 5, H]
+    included), the rest BF16 (project_out [H, 6], and the 64-wide inputs under K-quants); 1-D
+    tensors (norms, biases, the [H] learned tokens) F32."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, F, Nh, Nkv, D = (ccfg[k] for k in ("hidden_size", "intermediate_size", "n_heads", "n_kv_heads", "head_dim"))
+
+    def mat(name, shape, std=0.02):
+        K = shape[-1]
+        rows = int(np.prod(shape[:-1]))
+        w = torch.randn((rows, K), generator=g, device=device) * std
+        if K % _block_of(qtype) == 0:
+            return name, qtype, quantize_on_device(w, qtype), K, shape
+        b = w.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint16).reshape(shape)
+        return name, acb.BF16, b, K, shape
+
+    def vec(name, n, base=0.0, std=0.02):
+        v = (base + std * torch.randn(n, generator=g, device=device)).cpu().numpy().astype(np.float32)
+        return name, F32, v, n, (n,)
+
+    def stack(prefix, L):
+        for i in range(L):
+            p = f"{prefix}layers.{i}"
+            yield vec(f"{p}.input_layernorm.weight", H, 1.0, 0.01)
+            yield vec(f"{p}.post_attention_layernorm.weight", H, 1.0, 0.01)
+            yield mat(f"{p}.self_attn.q_proj.weight", (Nh * D, H))
+            yield mat(f"{p}.self_attn.k_proj.weight", (Nkv * D, H))
+            yield mat(f"{p}.self_attn.v_proj.weight", (Nkv * D, H))
+            yield mat(f"{p}.self_attn.o_proj.weight", (H, Nh * D))
+            yield vec(f"{p}.self_attn.q_norm.weight", D, 1.0, 0.01)
+            yield vec(f"{p}.self_attn.k_norm.weight", D, 1.0, 0.01)
+            yield mat(f"{p}.mlp.gate_proj.weight", (F, H))
+            yield mat(f"{p}.mlp.up_proj.weight", (F, H))
+            yield mat(f"{p}.mlp.down_proj.weight", (H, F))
+        yield vec(f"{prefix}norm.weight", H, 1.0, 0.01)
+
+    C = ccfg["latent_dim"]
+    yield mat("encoder.lyric_encoder.embed_tokens.weight", (H, ccfg["lyric_dim"]))
+    yield vec("encoder.lyric_encoder.embed_tokens.bias", H)
+    yield from stack("encoder.lyric_encoder.", ccfg["lyric_layers"])
+    yield mat("encoder.timbre_encoder.embed_tokens.weight", (H, C))
+    yield vec("encoder.timbre_encoder.embed_tokens.bias", H)
+    yield from stack("encoder.timbre_encoder.", ccfg["timbre_layers"])
+    if timbre_cls:
+        yield vec("encoder.timbre_encoder.special_token", H, 0.0, 1.0)
+    yield mat("encoder.text_projector.weight", (H, ccfg["text_dim"]))
+    yield mat("tokenizer.audio_acoustic_proj.weight", (H, C))
+    yield vec("tokenizer.audio_acoustic_proj.bias", H)
+    yield mat("tokenizer.attention_pooler.embed_tokens.weight", (H, H))
+    yield vec("tokenizer.attention_pooler.embed_tokens.bias", H)
+    yield vec("tokenizer.attention_pooler.special_token", H, 0.0, 1.0)
+    yield from stack("tokenizer.attention_pooler.", ccfg["tok_layers"])
+    # project_in drives the FSQ levels: a larger spread so that every level occurs
+    yield mat("tokenizer.quantizer.project_in.weight", (6, H), 0.05)
+    yield vec("tokenizer.quantizer.project_in.bias", 6, 0.0, 0.2)
+    yield mat("tokenizer.quantizer.project_out.weight", (H, 6), 0.5)
+    yield vec("tokenizer.quantizer.project_out.bias", H)
+    yield mat("detokenizer.embed_tokens.weight", (H, H))
+    yield vec("detokenizer.embed_tokens.bias", H)
+    yield mat("detokenizer.special_tokens", (1, 5, H), 1.0)
+    yield from stack("detokenizer.", ccfg["detok_layers"])
+    yield mat("detokenizer.proj_out.weight", (C, H))
+    yield vec("detokenizer.proj_out.bias", C)
+
+
 def write_dit_gguf(path: str, cfg: dict, qtype: int = Q8_0, seed: int = 0, device: str = "cuda",
-                   keep: dict | None = None, null_condition: bool = True) -> int:
+                   keep: dict | None = None, null_condition: bool = True, cond: dict | None = None,
+                   timbre_cls: bool = False, decoder: bool = True) -> int:
     """Write a DiT GGUF with the reference's metadata keys (dit.h:276-287). If `keep` is a dict,
-    the raw tensors are stored in it as name -> (qtype, raw, K, shape)."""
+    the raw tensors are stored in it as name -> (qtype, raw, K, shape). `cond` (a COND_TINY-like
+    dict) adds the condition encoder and FSQ tensors; timbre_cls writes the XL models'
+    acestep.encoder_hidden_size key and timbre special_token; decoder False leaves the
+    decoder.* tensors out (only null_condition_emb stays)."""
     import gguf
     w = gguf.GGUFWriter(path, "acestep-dit")
     a = "acestep-dit"
@@ -202,8 +287,18 @@ def write_dit_gguf(path: str, cfg: dict, qtype: int = Q8_0, seed: int = 0, devic
     w.add_uint32("acestep.audio_acoustic_hidden_dim", cfg["out_channels"])
     w.add_uint32("acestep.patch_size", cfg["patch_size"])
     w.add_uint32("acestep.sliding_window", cfg["sliding_window"])
+    if timbre_cls:
+        w.add_uint32("acestep.encoder_hidden_size", cfg["enc_hidden_size"])
     total = 0
-    for name, qt, raw, K, shape in dit_tensors(cfg, qtype, seed, device, null_condition):
+
+    def all_tensors():
+        for t in dit_tensors(cfg, qtype, seed, device, null_condition):
+            if decoder or not t[0].startswith("decoder."):
+                yield t
+        if cond is not None:
+            yield from cond_tensors(cond, qtype, seed + 7, device, timbre_cls)
+
+    for name, qt, raw, K, shape in all_tensors():
         if qt == F32:
             w.add_tensor(name, raw)
         elif qt == acb.BF16:

@@ -68,6 +68,7 @@ enum {
     ACB_DEVERR_ID_RANGE  = 1, /* get_rows id outside [0, n_rows) */
     ACB_DEVERR_POS_RANGE = 2, /* rope / kv position outside [0, max_pos) */
     ACB_DEVERR_TIMEOUT   = 4, /* a bounded device-side wait gave up */
+    ACB_DEVERR_CODE_RANGE = 8, /* a negative FSQ code (acb_fsq_project_out) */
 };
 
 /* ---- library ------------------------------------------------------------------------------ */
@@ -384,6 +385,32 @@ ACB_API acb_status acb_dit_dpm3m(float * xt, const float * vt, float * prev_vt, 
  * with that seed). The last step of a schedule is acb_dit_euler with last != 0. */
 ACB_API acb_status acb_dit_sde(float * xt, const float * vt, const float * noise, const float * tt, int64_t n,
                                acb_stream_t stream);
+
+/* ---- FSQ and sequence packing (the condition encoder and the FSQ (de)tokenizer) ------------- */
+
+/* out[g][n] = project_out(fsq_decode_index(codes[g]))[n] + bias[n] for G codes: the flat index is
+ * split into the 6 FSQ levels {8,8,8,5,5,5} (fsq_decode_index, src/fsq-detok.h:18-29: level /
+ * ((L-1)/2) - 1), rounded to the weight type and multiplied by w [N][6] (BF16, F16 or F32, the
+ * tokenizer.quantizer.project_out weight), products added in double and rounded once, then the
+ * f32 bias (NULL: none) -- ggml_mul_mat + ggml_add of src/fsq-detok.h:150-160, batched over every
+ * code. A negative code writes a zero row and sets ACB_DEVERR_CODE_RANGE. */
+ACB_API acb_status acb_fsq_project_out(const int32_t * codes, int G, const void * w, int w_type, int N,
+                                       const float * bias, float * out, int64_t ldo, int * err_flag,
+                                       acb_stream_t stream);
+/* codes[g] = fsq_encode_index(raw[g][0..5] + bias): tanh, level floor((L-1)(t+1)/2 + 0.5) clamped
+ * to [0, L-1], flat index with dimension 0 fastest (src/fsq-tok.h:42-60, 196-199). raw rows ld
+ * floats apart; bias f32 [6] or NULL. */
+ACB_API acb_status acb_fsq_quantize(const float * raw, int64_t ld, const float * bias, int G, int32_t * codes,
+                                    acb_stream_t stream);
+/* out[g*P + p][:] = a[g][:] + b[p][:] (f32 rows of H, H and the strides multiples of 4, pointers
+ * 16-byte aligned): ggml_add(ggml_repeat(embedded, special), special), src/fsq-detok.h:165-169. */
+ACB_API acb_status acb_rows_repeat_add(const float * a, int64_t lda, const float * b, int64_t ldb, int G, int P,
+                                       int H, float * out, int64_t ldo, acb_stream_t stream);
+/* out[g*(P+1)][:] = head[:], out[g*(P+1) + 1 + p][:] = src[g*P + p][:]: a learned token prepended
+ * to each group of P rows (ggml_concat(cls, x, 1), src/fsq-tok.h:181-184, src/cond-enc.h:256-259).
+ * Alignment as acb_rows_repeat_add. */
+ACB_API acb_status acb_rows_prepend(const float * head, const float * src, int64_t lds, int G, int P, int H,
+                                    float * out, int64_t ldo, acb_stream_t stream);
 
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 

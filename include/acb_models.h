@@ -89,6 +89,91 @@ ACB_API acb_status acb_qwen3_forward_hidden(acb_qwen3_enc * m, const float * d_h
 ACB_API acb_status acb_qwen3_embed_lookup(acb_qwen3_enc * m, const int32_t * token_ids, int S, float * output);
 ACB_API void       acb_qwen3_free(acb_qwen3_enc * m); /* qwen3_free :483 */
 
+/* ---- condition encoder (replaces src/cond-enc.h) --------------------------------------------- */
+
+typedef struct acb_cond acb_cond;
+
+/* Sizes of a loaded condition encoder: the packed output width, the two input widths, the stacks'
+ * depths and whether the timbre stack prepends its learned CLS token (XL models, the GGUF key
+ * acestep.encoder_hidden_size present). */
+typedef struct {
+    int hidden_size;   /* 2048: width of the packed encoder states */
+    int text_dim;      /* 1024: text_projector input (Qwen3-Embedding states) */
+    int lyric_dim;     /* 1024: lyric embed_tokens input */
+    int timbre_dim;    /* 64: timbre embed_tokens input (VAE latent channels) */
+    int lyric_layers;  /* 8 */
+    int timbre_layers; /* 4 */
+    int window;        /* 128: |i - j| <= window on the even layers of both stacks */
+    int timbre_cls;    /* 1 when the timbre stack prepends its CLS token */
+} acb_cond_config;
+
+/* cond_ggml_load (cond-enc.h:86-164) from the DiT GGUF: encoder.lyric_encoder.* (8 layers),
+ * encoder.timbre_encoder.* (4 layers, special_token when acestep.encoder_hidden_size > 0),
+ * encoder.text_projector.weight and null_condition_emb. Linears become resident 16-bit copies
+ * for the tensor-core GEMM as in acb_qwen3_load_text_encoder. */
+ACB_API acb_status acb_cond_load(const char * gguf_path, int device, acb_cond ** out);
+ACB_API acb_status acb_cond_get_config(const acb_cond * m, acb_cond_config * cfg);
+/* exact (default) / fast arithmetic of every linear and attention, as acb_qwen3_set_exact. */
+ACB_API acb_status acb_cond_set_exact(acb_cond * m, int exact);
+/* cond_ggml_forward (cond-enc.h:171-381). Host f32 inputs, rows contiguous: text_hidden
+ * [S_text][1024], lyric_embed [S_lyric][1024], timbre_feats [S_ref][64] (NULL or S_ref 0: no
+ * timbre). enc_hidden (caller-allocated, (S_lyric + (timbre ? 1 : 0) + S_text) * hidden_size
+ * floats) receives the packed states [lyric | timbre row 0 | text projection]; *out_enc_S their
+ * row count. S_lyric >= 1 and S_text >= 1 as in the reference. */
+ACB_API acb_status acb_cond_forward(acb_cond * m, const float * text_hidden, int S_text, const float * lyric_embed,
+                                    int S_lyric, const float * timbre_feats, int S_ref, float * enc_hidden,
+                                    int * out_enc_S);
+/* The same on device buffers, enqueued on `stream` (no host synchronisation; calls on one model
+ * must not overlap). */
+ACB_API acb_status acb_cond_forward_device(acb_cond * m, const float * d_text_hidden, int S_text,
+                                           const float * d_lyric_embed, int S_lyric, const float * d_timbre_feats,
+                                           int S_ref, float * d_enc_hidden, int * out_enc_S, acb_stream_t stream);
+/* null_condition_emb as f32 [hidden_size] (host): the unconditional row of classifier-free
+ * guidance (CondGGML.null_cond_emb). */
+ACB_API acb_status acb_cond_null_embedding(acb_cond * m, float * out);
+ACB_API void       acb_cond_free(acb_cond * m); /* cond_ggml_free :383 */
+
+/* ---- FSQ detokenizer and tokenizer (replace src/fsq-detok.h, src/fsq-tok.h) ------------------ */
+
+/* The FSQ alphabet: 6 dimensions of {8, 8, 8, 5, 5, 5} levels, 64000 codes. Host helpers with the
+ * reference's arithmetic: fsq_decode_index (fsq-detok.h:18-29) and fsq_encode_index
+ * (fsq-tok.h:42-60). */
+ACB_API void acb_fsq_decode_index(int index, float * out6);
+ACB_API int  acb_fsq_encode_index(const float * raw6);
+
+typedef struct acb_detok acb_detok;
+
+/* detok_ggml_load (fsq-detok.h:70-122): tokenizer.quantizer.project_out.*, detokenizer.* (2-layer
+ * bidirectional stack, special_tokens [5][2048], proj_out 2048 -> 64) from the DiT GGUF. */
+ACB_API acb_status acb_detok_load(const char * gguf_path, int device, acb_detok ** out);
+ACB_API acb_status acb_detok_set_exact(acb_detok * m, int exact);
+/* detok_ggml_decode (fsq-detok.h:128-212): codes [T_5Hz] (host) -> context_out [T_5Hz * 5][64]
+ * (host, caller-allocated). Every code is decoded in one batch (5 frames per code, attention
+ * within a code's frames). ACB_ERR_OUT_OF_RANGE for a negative code. */
+ACB_API acb_status acb_detok_decode(acb_detok * m, const int * codes, int T_5Hz, float * context_out);
+/* The same on device buffers (codes int32 [T_5Hz], out f32 [T_5Hz * 5][64]), enqueued on stream;
+ * a negative code gives a zero row and ACB_DEVERR_CODE_RANGE in the model's device flag, which
+ * acb_detok_decode checks. */
+ACB_API acb_status acb_detok_decode_device(acb_detok * m, const int32_t * d_codes, int T_5Hz, float * d_out,
+                                           acb_stream_t stream);
+ACB_API void       acb_detok_free(acb_detok * m); /* detok_ggml_free :215 */
+
+typedef struct acb_tok acb_tok;
+
+/* tok_ggml_load (fsq-tok.h:63-126): tokenizer.audio_acoustic_proj.*, tokenizer.attention_pooler.*
+ * (embed, special_token, 2-layer stack, norm) and tokenizer.quantizer.project_in.*. */
+ACB_API acb_status acb_tok_load(const char * gguf_path, int device, acb_tok ** out);
+ACB_API acb_status acb_tok_set_exact(acb_tok * m, int exact);
+/* tok_ggml_encode (fsq-tok.h:133-238): latents [T_25Hz][64] (host) padded to a multiple of 5 with
+ * the first rows of silence_latent ([>= 4][64], required when T_25Hz % 5 != 0) -> codes_out
+ * [(T_25Hz + 4) / 5] (host); *out_T_5Hz receives the count. All groups run as one batch. */
+ACB_API acb_status acb_tok_encode(acb_tok * m, const float * latents, int T_25Hz, int * codes_out,
+                                  const float * silence_latent, int * out_T_5Hz);
+/* The same on device buffers: latents f32 [T_5Hz * 5][64] already padded, codes int32 [T_5Hz]. */
+ACB_API acb_status acb_tok_encode_device(acb_tok * m, const float * d_latents, int T_5Hz, int32_t * d_codes,
+                                         acb_stream_t stream);
+ACB_API void       acb_tok_free(acb_tok * m); /* tok_ggml_free :241 */
+
 /* ---- ACE-Step DiT (replaces src/dit.h, src/dit-graph.h, src/dit-sampler.h) ------------------- */
 
 typedef struct acb_dit acb_dit;

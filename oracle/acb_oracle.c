@@ -982,3 +982,38 @@ void orc_timestep_embedding(float t, int dim, int max_period, float * out) {
         out[dim - 1] = 0.0f;
     }
 }
+
+/* ---- FSQ (src/fsq-detok.h:14-29, src/fsq-tok.h:42-60) ---- */
+
+static const int orc_fsq_levels[6] = { 8, 8, 8, 5, 5, 5 };
+
+/* fsq_decode_index: dimension d's level (index / prod(L_<d)) % L_d mapped to level / ((L-1)/2) - 1 */
+void orc_fsq_decode_index(int index, float * out6) {
+    int stride = 1;
+    for (int d = 0; d < 6; d++) {
+        int   L      = orc_fsq_levels[d];
+        float half_L = (float) (L - 1) / 2.0f;
+        out6[d]      = (float) ((index / stride) % L) / half_L - 1.0f;
+        stride *= L;
+    }
+}
+
+/* fsq_encode_index: level floor((L-1) * (tanh(x) + 1) / 2 + 0.5) clamped to [0, L-1], flat index
+ * with dimension 0 fastest */
+int orc_fsq_encode_index(const float * raw6) {
+    int index = 0, mult = 1;
+    for (int d = 0; d < 6; d++) {
+        int   L    = orc_fsq_levels[d];
+        float t    = tanhf(raw6[d]);
+        int   code = (int) floorf((float) (L - 1) * (t + 1.0f) / 2.0f + 0.5f);
+        if (code < 0) {
+            code = 0;
+        }
+        if (code >= L) {
+            code = L - 1;
+        }
+        index += code * mult;
+        mult *= L;
+    }
+    return index;
+}

@@ -124,6 +124,11 @@ void orc_attention(const float * q, int64_t q_tok_stride, const void * k, const 
 /* Sinusoidal timestep embedding (ggml_timestep_embedding, dim even): out[dim]. */
 void orc_timestep_embedding(float t, int dim, int max_period, float * out);
 
+/* FSQ alphabet {8,8,8,5,5,5}: fsq_decode_index (src/fsq-detok.h:18-29) and fsq_encode_index
+ * (src/fsq-tok.h:42-60, libm tanhf). */
+void orc_fsq_decode_index(int index, float * out6);
+int  orc_fsq_encode_index(const float * raw6);
+
 /* Thread control for the CPU baseline (0 = OpenMP default). */
 void orc_set_threads(int n);
 int  orc_get_threads(void);

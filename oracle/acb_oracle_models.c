@@ -61,8 +61,10 @@ typedef struct {
     const int32_t * pos;         /* position of each token */
 } attn_ctx;
 
+/* One layer over S rows. Encoder (ac->kv NULL): the rows are B sequences of S / B rows, attention
+ * within each sequence under the additive mask_enc [S/B][S/B] (NULL: none). */
 static int qwen3_layer(const orc_qwen3 * m, const orc_qwen3_layer * ly, float * hidden, int S, const float * rope,
-                       const attn_ctx * ac, const float * mask_enc) {
+                       const attn_ctx * ac, const float * mask_enc, int B) {
     const int H = m->H, D = m->D, Nh = m->Nh, Nkv = m->Nkv, F = m->F;
     const int qd = Nh * D, kvd = Nkv * D, qkvd = qd + 2 * kvd;
     float *   norm = fbuf((int64_t) S * H);
@@ -103,7 +105,12 @@ static int qwen3_layer(const orc_qwen3 * m, const orc_qwen3_layer * ly, float * 
     }
     const float scale = 1.0f / sqrtf((float) D);
     if (!ac->kv) {
-        orc_attention(q, qd, k, v, ORC_F32, kvd, D, mask_enc, att, qd, S, S, Nh, Nkv, D, scale);
+        const int Ss = S / B;
+        for (int b = 0; b < B; b++) {
+            const int64_t r = (int64_t) b * Ss;
+            orc_attention(q + r * qd, qd, k + r * kvd, v + r * kvd, ORC_F32, kvd, D, mask_enc, att + r * qd, qd, Ss, Ss,
+                          Nh, Nkv, D, scale);
+        }
     } else {
         orc_kv *      kv  = ac->kv;
         const int64_t hs  = (int64_t) kv->max_seq * D;            /* head stride */
@@ -178,32 +185,49 @@ static int qwen3_layer(const orc_qwen3 * m, const orc_qwen3_layer * ly, float * 
     return rc ? -1 : 0;
 }
 
-int orc_qwen3_layers(const orc_qwen3 * m, float * hidden, int S, int l0, int l1, int causal, float * out) {
-    if (l0 < 0 || l1 > m->n_layers || l0 > l1) {
+int orc_qwen3_layers_ex(const orc_qwen3 * m, float * hidden, int B, int S, int l0, int l1, int causal, int window,
+                        float * out) {
+    if (l0 < 0 || l1 > m->n_layers || l0 > l1 || B <= 0 || S <= 0) {
         return -1;
     }
-    int32_t * pos  = (int32_t *) malloc(sizeof(int32_t) * S);
-    float *   rope = fbuf((int64_t) S * m->D);
+    const int R    = B * S;
+    int32_t * pos  = (int32_t *) malloc(sizeof(int32_t) * R);
+    float *   rope = fbuf((int64_t) R * m->D);
     float *   mask = causal ? fbuf((int64_t) S * S) : NULL;
+    /* the bidirectional sliding window of the even layers: |i - j| <= window (cond-enc.h:298-312) */
+    float *   slide = (!causal && window > 0) ? fbuf((int64_t) S * S) : NULL;
     for (int i = 0; i < S; i++) {
-        pos[i] = i;
-        for (int j = 0; causal && j < S; j++) {
-            mask[(int64_t) i * S + j] = (j <= i) ? 0.0f : -INFINITY;
+        for (int j = 0; j < S; j++) {
+            if (mask) {
+                mask[(int64_t) i * S + j] = (j <= i) ? 0.0f : -INFINITY;
+            }
+            if (slide) {
+                slide[(int64_t) i * S + j] = abs(i - j) <= window ? 0.0f : -INFINITY;
+            }
         }
     }
-    orc_rope_cache(rope, pos, S, m->D, m->rope_theta);
+    for (int i = 0; i < R; i++) {
+        pos[i] = i % S;
+    }
+    orc_rope_cache(rope, pos, R, m->D, m->rope_theta);
     attn_ctx ac = { 0 };
     int      rc = 0;
     for (int l = l0; l < l1 && rc == 0; l++) {
-        rc = qwen3_layer(m, &m->layers[l], hidden, S, rope, &ac, mask);
+        const float * lm = causal ? mask : (slide && l % 2 == 0 ? slide : NULL);
+        rc               = qwen3_layer(m, &m->layers[l], hidden, R, rope, &ac, lm, B);
     }
     if (out) {
-        orc_rms_norm(hidden, (const float *) m->final_norm.data, out, S, m->H, m->eps);
+        orc_rms_norm(hidden, (const float *) m->final_norm.data, out, R, m->H, m->eps);
     }
     free(pos);
     free(rope);
     free(mask);
+    free(slide);
     return rc;
+}
+
+int orc_qwen3_layers(const orc_qwen3 * m, float * hidden, int S, int l0, int l1, int causal, float * out) {
+    return orc_qwen3_layers_ex(m, hidden, 1, S, l0, l1, causal, 0, out);
 }
 
 int orc_qwen3_encode(const orc_qwen3 * m, const int32_t * ids, int S, float * out) {
@@ -245,7 +269,7 @@ int orc_qw3lm_prefill(const orc_qwen3 * m, orc_kv * kv, int set, int kv_pos, con
     int      rc = 0;
     for (int l = 0; l < m->n_layers && rc == 0; l++) {
         ac.layer = l;
-        rc       = qwen3_layer(m, &m->layers[l], hidden, n, rope, &ac, NULL);
+        rc       = qwen3_layer(m, &m->layers[l], hidden, n, rope, &ac, NULL, 1);
     }
     float * fin = fbuf((int64_t) n * H);
     orc_rms_norm(hidden, (const float *) m->final_norm.data, fin, n, H, m->eps);
@@ -281,7 +305,7 @@ int orc_qw3lm_decode(const orc_qwen3 * m, orc_kv * kv, int set0, const int32_t *
     int      rc = 0;
     for (int l = 0; l < m->n_layers && rc == 0; l++) {
         ac.layer = l;
-        rc       = qwen3_layer(m, &m->layers[l], hidden, N, rope, &ac, NULL);
+        rc       = qwen3_layer(m, &m->layers[l], hidden, N, rope, &ac, NULL, 1);
     }
     float * fin = fbuf((int64_t) N * H);
     orc_rms_norm(hidden, (const float *) m->final_norm.data, fin, N, H, m->eps);

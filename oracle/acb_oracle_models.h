@@ -66,6 +66,14 @@ int orc_qwen3_encode(const orc_qwen3 * m, const int32_t * ids, int S, float * ou
  * (cond_ggml_forward) and per-layer parity checks use it. */
 int orc_qwen3_layers(const orc_qwen3 * m, float * hidden, int S, int l0, int l1, int causal, float * out);
 
+/* orc_qwen3_layers over B independent sequences of S rows each (hidden [B*S][H], positions
+ * 0..S-1 in every sequence, attention within a sequence), and with window > 0 on a bidirectional
+ * stack the sliding-window mask |i - j| <= window on the even layers (the lyric and timbre
+ * encoders, src/cond-enc.h:203-212, 263-272). B > 1 is the reference's loop of one graph per
+ * group (fsq-tok.h:208-223, fsq-detok.h:193-205) done as one call: every linear is row-wise. */
+int orc_qwen3_layers_ex(const orc_qwen3 * m, float * hidden, int B, int S, int l0, int l1, int causal, int window,
+                        float * out);
+
 /* LM prefill of n tokens into kv set `set` starting at position kv_pos; writes the f16 K/V,
  * returns the logits of the last token in logits[V] (or lm rows [lm_offset, lm_offset+lm_count)
  * when lm_count > 0). If hidden_out is non-NULL it receives the final-normed hidden rows

@@ -59,6 +59,8 @@ def lib():
             "orc_set_mul_mat_mode": (None, [I]),
             "orc_get_mul_mat_mode": (I, []),
             "orc_get_threads": (I, []),
+            "orc_fsq_decode_index": (None, [I, P]),
+            "orc_fsq_encode_index": (I, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -314,6 +316,8 @@ def _models_lib():
         L.orc_qwen3_encode.argtypes = [C.POINTER(Qwen3), P, I, P]
         L.orc_qwen3_layers.restype = I
         L.orc_qwen3_layers.argtypes = [C.POINTER(Qwen3), P, I, I, I, I, P]
+        L.orc_qwen3_layers_ex.restype = I
+        L.orc_qwen3_layers_ex.argtypes = [C.POINTER(Qwen3), P, I, I, I, I, I, I, P]
         L.orc_qw3lm_prefill.restype = I
         L.orc_qw3lm_prefill.argtypes = [C.POINTER(Qwen3), C.POINTER(KV), I, I, P, I, P, I, I, P]
         L.orc_qw3lm_decode.restype = I
@@ -357,9 +361,13 @@ class OracleQwen3:
                     continue
                 qt, raw, K, N = weights[key]
                 setattr(self.layers[i], f[0], tensor(raw, qt, K, N, self.keep))
-        qt, raw, K, N = weights["embed"]
-        self.embed_src = (qt, raw, K, N)
-        emb = tensor(raw, qt, K, N, self.keep)
+        if "embed" in weights:
+            qt, raw, K, N = weights["embed"]
+            self.embed_src = (qt, raw, K, N)
+            emb = tensor(raw, qt, K, N, self.keep)
+        else:  # a stack fed by a projection (condition encoder, FSQ models): no table
+            self.embed_src = None
+            emb = Tensor(F32, None, 0, 0)
         qt, raw, K, N = weights["final_norm"]
         fn = tensor(raw, qt, K, N, self.keep)
         self.m = Qwen3(L, cfg["H"], cfg["F"], cfg["Nh"], cfg["Nkv"], cfg["D"], cfg["V"], cfg["rope_theta"],
@@ -381,14 +389,16 @@ class OracleQwen3:
         assert rc == 0
         return out
 
-    def run_layers(self, hidden, l0, l1, causal=True, final_norm=False):
-        """Layers [l0, l1) from hidden [S][H] (returned updated; with final_norm also the normed
-        output): qwen3_build_layers over a layer range."""
+    def run_layers(self, hidden, l0, l1, causal=True, final_norm=False, batch=1, window=0):
+        """Layers [l0, l1) from hidden [batch*S][H] (returned updated; with final_norm also the
+        normed output): qwen3_build_layers over a layer range, `batch` independent sequences of S
+        rows, and on a bidirectional stack with window > 0 the sliding window of the even layers."""
         h = np.array(hidden, dtype=np.float32, copy=True, order="C")
-        S = h.shape[0]
+        R = h.shape[0]
+        assert R % batch == 0
         out = np.empty_like(h) if final_norm else None
-        rc = _models_lib().orc_qwen3_layers(C.byref(self.m), _p(h), S, l0, l1, int(causal),
-                                            _p(out) if out is not None else None)
+        rc = _models_lib().orc_qwen3_layers_ex(C.byref(self.m), _p(h), batch, R // batch, l0, l1, int(causal),
+                                               window, _p(out) if out is not None else None)
         assert rc == 0
         return (h, out) if final_norm else h
 
@@ -683,3 +693,151 @@ def sde_step(xt, vt, noise, t_curr, t_next):
     a = (f(t_next) * np.asarray(noise, np.float32)).astype(np.float32)
     b = ((f(1.0) - f(t_next)) * x0).astype(np.float32)
     return (a + b).astype(np.float32)
+
+
+# ---- condition encoder and FSQ models (src/cond-enc.h, src/fsq-detok.h, src/fsq-tok.h) ----------
+
+def fsq_decode_index(index: int) -> np.ndarray:
+    out = np.empty(6, dtype=np.float32)
+    lib().orc_fsq_decode_index(int(index), _p(out))
+    return out
+
+
+def fsq_encode_index(raw6) -> int:
+    r = np.ascontiguousarray(raw6, dtype=np.float32)
+    return int(lib().orc_fsq_encode_index(_p(r)))
+
+
+def stack_from_gguf_tensors(tensors, prefix):
+    """OracleQwen3 (no embedding table) over the stack `prefix`layers.{i}.* / `prefix`norm.weight,
+    sizes from the tensor shapes; tensors {name: (qtype, raw, K, shape)} as synthetic's keep."""
+    L = 0
+    while f"{prefix}layers.{L}.input_layernorm.weight" in tensors:
+        L += 1
+    D = tensors[f"{prefix}layers.0.self_attn.q_norm.weight"][2]
+    H = tensors[f"{prefix}norm.weight"][2]
+
+    def rows(t):
+        return int(np.prod(t[3])) // t[2]
+
+    cfg = dict(num_hidden_layers=L, hidden_size=H, head_dim=D,
+               intermediate_size=rows(tensors[f"{prefix}layers.0.mlp.gate_proj.weight"]),
+               num_attention_heads=rows(tensors[f"{prefix}layers.0.self_attn.q_proj.weight"]) // D,
+               num_key_value_heads=rows(tensors[f"{prefix}layers.0.self_attn.k_proj.weight"]) // D,
+               vocab_size=0, rope_theta=1000000.0, rms_norm_eps=1e-6)
+    w = {}
+    for i in range(L):
+        p = f"{prefix}layers.{i}"
+        w[f"layers.{i}.attn_norm"] = _t4(tensors[f"{p}.input_layernorm.weight"])
+        w[f"layers.{i}.post_norm"] = _t4(tensors[f"{p}.post_attention_layernorm.weight"])
+        w[f"layers.{i}.q_norm"] = _t4(tensors[f"{p}.self_attn.q_norm.weight"])
+        w[f"layers.{i}.k_norm"] = _t4(tensors[f"{p}.self_attn.k_norm.weight"])
+        w[f"layers.{i}.o"] = _t4(tensors[f"{p}.self_attn.o_proj.weight"])
+        w[f"layers.{i}.down"] = _t4(tensors[f"{p}.mlp.down_proj.weight"])
+        for n in "qkv":
+            w[f"layers.{i}.{n}"] = _t4(tensors[f"{p}.self_attn.{n}_proj.weight"])
+        w[f"layers.{i}.gate"] = _t4(tensors[f"{p}.mlp.gate_proj.weight"])
+        w[f"layers.{i}.up"] = _t4(tensors[f"{p}.mlp.up_proj.weight"])
+    w["final_norm"] = _t4(tensors[f"{prefix}norm.weight"])
+    oc = dict(n_layers=L, H=H, F=cfg["intermediate_size"], Nh=cfg["num_attention_heads"],
+              Nkv=cfg["num_key_value_heads"], D=D, V=0, rope_theta=cfg["rope_theta"], eps=cfg["rms_norm_eps"])
+    return OracleQwen3(oc, w)
+
+
+def _t4(t):
+    """(qtype, raw, K, shape) -> (qtype, raw, K, N) for OracleQwen3."""
+    qt, raw, K, shape = t
+    return qt, raw, K, int(np.prod(shape)) // K
+
+
+def _linear(t, x, bias=None):
+    """ggml_mul_mat(W, x) (+ ggml_add(bias)) for a tensor (qtype, raw, K, shape)."""
+    qt, raw, K, shape = t
+    N = int(np.prod(shape)) // K
+    y = mul_mat(qt, raw, N, K, np.ascontiguousarray(x, dtype=np.float32).reshape(-1, K))
+    if bias is not None:
+        y = y + _f32_of(bias).reshape(1, N)
+    return y
+
+
+def _f32_of(t):
+    """A small tensor as float32 (gf_load_tensor_f32, or ggml_cast of a quantised one)."""
+    qt, raw, K, shape = t
+    if qt == F32:
+        return np.asarray(raw, dtype=np.float32).reshape(-1, K)
+    if qt == BF16:
+        return bf16_bits_to_f32(np.asarray(raw, dtype=np.uint16)).reshape(-1, K)
+    if qt == F16:
+        return np.asarray(raw, dtype=np.uint16).view(np.float16).astype(np.float32).reshape(-1, K)
+    return dequantize(np.asarray(raw).reshape(-1, row_bytes(qt, K)), qt, K)
+
+
+class OracleCond:
+    """cond_ggml_forward (src/cond-enc.h:171-381) over raw tensors: lyric stack with the window
+    128 mask on even layers, timbre stack (CLS prepended when timbre_cls), text projector."""
+
+    def __init__(self, tensors, timbre_cls=False):
+        self.t = tensors
+        self.cls = timbre_cls
+        self.lyric = stack_from_gguf_tensors(tensors, "encoder.lyric_encoder.")
+        self.timbre = stack_from_gguf_tensors(tensors, "encoder.timbre_encoder.")
+
+    def forward(self, text, lyric, timbre=None, window=128):
+        t = self.t
+        h = _linear(t["encoder.lyric_encoder.embed_tokens.weight"], lyric,
+                    t["encoder.lyric_encoder.embed_tokens.bias"])
+        _, lyr = self.lyric.run_layers(h, 0, self.lyric.cfg["n_layers"], causal=False, final_norm=True,
+                                       window=window)
+        parts = [lyr]
+        if timbre is not None and len(timbre) > 0:
+            th = _linear(t["encoder.timbre_encoder.embed_tokens.weight"], timbre,
+                         t["encoder.timbre_encoder.embed_tokens.bias"])
+            if self.cls:
+                th = np.concatenate([_f32_of(t["encoder.timbre_encoder.special_token"]).reshape(1, -1), th])
+            _, tim = self.timbre.run_layers(th, 0, self.timbre.cfg["n_layers"], causal=False, final_norm=True,
+                                            window=window)
+            parts.append(tim[:1])
+        parts.append(_linear(t["encoder.text_projector.weight"], text))
+        return np.concatenate(parts).astype(np.float32)
+
+
+class OracleDetok:
+    """detok_ggml_decode (src/fsq-detok.h:128-212), all groups as one batch of 5-row sequences."""
+
+    def __init__(self, tensors):
+        self.t = tensors
+        self.stack = stack_from_gguf_tensors(tensors, "detokenizer.")
+
+    def decode(self, codes):
+        t = self.t
+        G = len(codes)
+        x = np.stack([fsq_decode_index(c) for c in codes])
+        q = _linear(t["tokenizer.quantizer.project_out.weight"], x, t["tokenizer.quantizer.project_out.bias"])
+        e = _linear(t["detokenizer.embed_tokens.weight"], q, t["detokenizer.embed_tokens.bias"])
+        sp = _f32_of(t["detokenizer.special_tokens"])
+        h = (e[:, None, :] + sp[None, :, :]).reshape(G * 5, -1).astype(np.float32)
+        _, y = self.stack.run_layers(h, 0, self.stack.cfg["n_layers"], causal=False, final_norm=True, batch=G)
+        return _linear(t["detokenizer.proj_out.weight"], y, t["detokenizer.proj_out.bias"])
+
+
+class OracleTok:
+    """tok_ggml_encode (src/fsq-tok.h:133-238) on latents already padded to 5 * G frames; returns
+    (codes [G], pre-activation values [G][6])."""
+
+    def __init__(self, tensors):
+        self.t = tensors
+        self.stack = stack_from_gguf_tensors(tensors, "tokenizer.attention_pooler.")
+
+    def encode(self, latents):
+        t = self.t
+        G = latents.shape[0] // 5
+        p = _linear(t["tokenizer.audio_acoustic_proj.weight"], latents, t["tokenizer.audio_acoustic_proj.bias"])
+        e = _linear(t["tokenizer.attention_pooler.embed_tokens.weight"], p,
+                    t["tokenizer.attention_pooler.embed_tokens.bias"])
+        cls = _f32_of(t["tokenizer.attention_pooler.special_token"]).reshape(1, 1, -1)
+        H = e.shape[1]
+        h = np.concatenate([np.broadcast_to(cls, (G, 1, H)), e.reshape(G, 5, H)], axis=1).reshape(G * 6, H)
+        _, y = self.stack.run_layers(np.ascontiguousarray(h, dtype=np.float32), 0, self.stack.cfg["n_layers"],
+                                     causal=False, final_norm=True, batch=G)
+        raw = _linear(t["tokenizer.quantizer.project_in.weight"], y[0::6], t["tokenizer.quantizer.project_in.bias"])
+        return np.array([fsq_encode_index(r) for r in raw], dtype=np.int32), raw
