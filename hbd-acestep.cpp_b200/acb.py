@@ -148,6 +148,8 @@ def lib():
             "acb_gemm_qkv_planes": (I, [P, I64, P, I64, I64, I64, I, I, P, P, F, P, P, I, I64, P, I64, I64, P, I64, I64,
                                         I, P, P]),
             "acb_gemm_pair_clusters": (I, [I]),
+            "acb_sample_work_bytes": (C.c_size_t, [I, I]),
+            "acb_sample_top_k_p": (I, [P, I64, P, I64, F, I, I64, I, I, F, F, I, P, P, P, P]),
             "acb_fsq_project_out": (I, [P, I, P, I, I, P, P, I64, P, P]),
             "acb_fsq_quantize": (I, [P, I64, P, I, P, P]),
             "acb_rows_repeat_add": (I, [P, I64, P, I64, I, I, I, P, I64, P]),
@@ -430,6 +432,24 @@ class QW3LM:
             self.h, ids.ctypes.data, sets.ctypes.data, ids.size, out.ctypes.data, lm_offset, lm_count))
         return out
 
+    def forward_batch_sample(self, ids, kv_sets, n_active, use_cfg, cfg_scale, eos_idx, code_offset, n_codes,
+                             temperature, top_p, top_k, u=None, lm_offset=0, lm_count=0):
+        """Device-sampled phase-2 step: compact indices [n_active] (0 = EOS, 1 + c = code c)."""
+        np = self.np
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        sets = np.ascontiguousarray(kv_sets, dtype=np.int32)
+        uu = None if u is None else np.ascontiguousarray(u, dtype=np.float32)
+        out = np.empty(n_active, dtype=np.int32)
+        fn = lib().acb_qw3lm_forward_batch_sample
+        fn.restype = C.c_int
+        fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_int, C.c_int, C.c_int,
+                       C.c_int, C.c_int, C.c_float, C.c_float, C.c_int, C.c_void_p, C.c_void_p]
+        _check("acb_qw3lm_forward_batch_sample", fn(
+            self.h, ids.ctypes.data, sets.ctypes.data, n_active, int(bool(use_cfg)), cfg_scale, lm_offset, lm_count,
+            eos_idx, code_offset, n_codes, temperature, top_p, top_k, None if uu is None else uu.ctypes.data,
+            out.ctypes.data))
+        return out
+
     def generate_greedy(self, last_ids, set0, n_steps, want_margins=False):
         np = self.np
         last = np.ascontiguousarray(last_ids, dtype=np.int32)
@@ -628,6 +648,24 @@ class Qwen3Encoder:
         _check("acb_qwen3_embed_lookup", lib().acb_qwen3_embed_lookup(self.h, ids.ctypes.data, ids.size,
                                                                       out.ctypes.data))
         return out
+
+
+def sample_top_k_p(logits, temperature, top_p, top_k, u=None, uncond=None, cfg_scale=1.0, col0=-1, span_off=0,
+                   span_len=None, stream=None):
+    """Device sample_top_k_p over the rows of logits [rows][ld] (see acb.h): returns int32 [rows]
+    indices into the compacted row [col0?] + [span_off, span_off + span_len)."""
+    import torch
+    rows, ld = logits.shape
+    if span_len is None:
+        span_len = ld - span_off
+    Vc = (1 if col0 >= 0 else 0) + span_len
+    work = torch.empty(max(1, lib().acb_sample_work_bytes(rows, Vc)) // 4, dtype=torch.float32, device=logits.device)
+    idx = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _check("acb_sample_top_k_p", lib().acb_sample_top_k_p(
+        _ptr(logits), ld, None if uncond is None else _ptr(uncond), 0 if uncond is None else uncond.shape[1],
+        float(cfg_scale), int(col0), int(span_off), int(span_len), rows, float(temperature), float(top_p),
+        int(top_k), None if u is None else _ptr(u), _ptr(work), _ptr(idx), _stream(stream)))
+    return idx
 
 
 def fsq_decode_index(index: int):

@@ -61,6 +61,7 @@ struct acb_qw3lm {
     int                  cap_tok     = 0;
     int                  max_split   = 1;
     DevBuf hidden, qkv, q, scores, smax, part, att, tickets, gu, logits, ids, pos, err, hist_base, hist, mhist, amax;
+    DevBuf samp_work, samp_u, samp_idx;  // device sampling (acb_qw3lm_forward_batch_sample)
     int32_t *                           h_ids = nullptr;
     int32_t *                           h_pos = nullptr;
     std::map<long long, cudaGraphExec_t> graphs;
@@ -629,9 +630,11 @@ extern "C" acb_status acb_qw3lm_forward(acb_qw3lm * m, const int32_t * token_ids
     return ACB_OK;
 }
 
-extern "C" acb_status acb_qw3lm_forward_batch(acb_qw3lm * m, const int32_t * token_ids, const int32_t * kv_sets,
-                                              int N, float * logits, int lm_offset, int lm_count) {
-    if (!m || !token_ids || !kv_sets || !logits || N <= 0 || N > kMaxSets) {
+// One decode step for N consecutive sets; the logits [N][*out_v] stay in m->logits and the sets'
+// positions advance once the step has been enqueued.
+static acb_status forward_batch_dev(acb_qw3lm * m, const int32_t * token_ids, const int32_t * kv_sets, int N,
+                                    int lm_offset, int lm_count, int * out_v_ret) {
+    if (!m || !token_ids || !kv_sets || N <= 0 || N > kMaxSets) {
         return ACB_ERR_INVALID_ARG;
     }
     const int set0 = kv_sets[0];
@@ -665,12 +668,58 @@ extern "C" acb_status acb_qw3lm_forward_batch(acb_qw3lm * m, const int32_t * tok
             ((long long) N << 40) | ((long long) set0 << 32) | ((long long) (head == m->embed ? 0 : 1) << 31);
         ACB_TRY(run_graph(m, key, N, set0, head, out_v, false, true));
     }
-    cudaMemcpyAsync(logits, m->logits.p, sizeof(float) * (size_t) N * out_v, cudaMemcpyDeviceToHost, m->st);
-    ACB_TRY(sync(m));
     for (int i = 0; i < N; i++) {
         m->kv_pos[set0 + i]++;
     }
+    *out_v_ret = out_v;
     return ACB_OK;
+}
+
+extern "C" acb_status acb_qw3lm_forward_batch(acb_qw3lm * m, const int32_t * token_ids, const int32_t * kv_sets,
+                                              int N, float * logits, int lm_offset, int lm_count) {
+    if (!logits) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    int out_v = 0;
+    ACB_TRY(forward_batch_dev(m, token_ids, kv_sets, N, lm_offset, lm_count, &out_v));
+    cudaMemcpyAsync(logits, m->logits.p, sizeof(float) * (size_t) N * out_v, cudaMemcpyDeviceToHost, m->st);
+    return sync(m);
+}
+
+extern "C" acb_status acb_qw3lm_forward_batch_sample(acb_qw3lm * m, const int32_t * token_ids,
+                                                     const int32_t * kv_sets, int n_active, int use_cfg,
+                                                     float cfg_scale, int lm_offset, int lm_count, int eos_idx,
+                                                     int code_offset, int n_codes, float temperature, float top_p,
+                                                     int top_k, const float * u, int32_t * sampled) {
+    if (!m || !sampled || n_active <= 0 || n_codes < 0 || (temperature > 0.0f && !u)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int N     = use_cfg ? 2 * n_active : n_active;
+    int       out_v = 0;
+    ACB_TRY(forward_batch_dev(m, token_ids, kv_sets, N, lm_offset, lm_count, &out_v));
+    if (eos_idx < 0 || eos_idx >= out_v || code_offset < 0 || code_offset + n_codes > out_v) {
+        set_last_error("EOS / audio-code columns outside the logit row");
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int    Vc = 1 + n_codes;
+    const size_t wb = acb_sample_work_bytes(n_active, Vc);
+    if ((m->samp_work.bytes < wb && m->samp_work.alloc(wb, false) != ACB_OK) ||
+        (!m->samp_u.p && m->samp_u.alloc((size_t) kMaxSets * 4, false) != ACB_OK) ||
+        (!m->samp_idx.p && m->samp_idx.alloc((size_t) kMaxSets * 4, false) != ACB_OK)) {
+        set_last_error("sampling scratch allocation failed");
+        return ACB_ERR_OOM;
+    }
+    if (u && cudaMemcpyAsync(m->samp_u.p, u, sizeof(float) * n_active, cudaMemcpyHostToDevice, m->st) !=
+                 cudaSuccess) {
+        return ACB_ERR_CUDA;
+    }
+    const float * lg = m->logits.as<float>();
+    ACB_TRY(acb_sample_top_k_p(lg, out_v, use_cfg ? lg + (size_t) n_active * out_v : nullptr, out_v, cfg_scale,
+                               eos_idx, code_offset, n_codes, n_active, temperature, top_p, top_k,
+                               u ? m->samp_u.as<float>() : nullptr, m->samp_work.as<float>(),
+                               m->samp_idx.as<int32_t>(), (acb_stream_t) m->st));
+    cudaMemcpyAsync(sampled, m->samp_idx.p, sizeof(int32_t) * n_active, cudaMemcpyDeviceToHost, m->st);
+    return sync(m);
 }
 
 extern "C" acb_status acb_qw3lm_generate_greedy(acb_qw3lm * m, const int32_t * last_ids, int set0, int N,

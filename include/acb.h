@@ -412,6 +412,27 @@ ACB_API acb_status acb_rows_repeat_add(const float * a, int64_t lda, const float
 ACB_API acb_status acb_rows_prepend(const float * head, const float * src, int64_t lds, int G, int P, int H,
                                     float * out, int64_t ldo, acb_stream_t stream);
 
+/* ---- LM token sampling ------------------------------------------------------------------------ */
+
+/* sample_top_k_p (src/sampling.h:30-133) for `rows` sequences on the device, one CTA each, with the
+ * phase-2 targeted CFG and compaction in front (src/pipeline-lm.cpp:474-497). Row r's sampled row
+ * is x[c] for c < Vc = (col0 >= 0) + span_len: column col0 first (the EOS logit), then columns
+ * span_off .. span_off + span_len - 1 (the audio codes; col0 = -1, span_off 0, span_len V for a
+ * whole row); with uncond (rows uld floats apart) x = u + cfg_scale * (x - u) first. Then
+ * temperature (<= 0: greedy, first maximum), top_k (0: off), top_p (outside (0, 1): off) and the
+ * multinomial draw r = u[r] * sum with u[r] the canonical uniform that the reference's
+ * std::uniform_real_distribution<float>(0, sum) takes from the sequence's mt19937
+ * (std::generate_canonical<float, 24>; unused and may be NULL when greedy). idx[r] receives the
+ * index c in the compacted row. work: acb_sample_work_bytes(rows, Vc) bytes of device scratch.
+ * Reductions run in a fixed order (deterministic); the reference's single-thread sums round
+ * differently, which can change a draw only when r or top_p falls within rounding of a boundary.
+ * Equal probabilities at the top_p boundary are all kept. */
+ACB_API size_t     acb_sample_work_bytes(int rows, int Vc);
+ACB_API acb_status acb_sample_top_k_p(const float * logits, int64_t ld, const float * uncond, int64_t uld,
+                                      float cfg_scale, int col0, int64_t span_off, int span_len, int rows,
+                                      float temperature, float top_p, int top_k, const float * u, float * work,
+                                      int32_t * idx, acb_stream_t stream);
+
 /* ---- decode path (configs 3 and 5) --------------------------------------------------------- */
 
 enum {

@@ -376,6 +376,19 @@ ACB_API acb_status acb_qw3lm_forward(acb_qw3lm * m, const int32_t * token_ids, i
 ACB_API acb_status acb_qw3lm_forward_batch(acb_qw3lm * m, const int32_t * token_ids, const int32_t * kv_sets, int N,
                                            float * logits, int lm_offset, int lm_count);
 
+/* The phase-2 decode step of src/pipeline-lm.cpp:455-497 with its sampling on the device: one
+ * acb_qw3lm_forward_batch over n_active sets (2 * n_active with use_cfg: the conditional sets
+ * first, then the unconditional ones, the reference's layout), then for each active sequence the
+ * targeted CFG lu + cfg_scale * (lc - lu) over its [eos_idx] + [code_offset, code_offset + n_codes)
+ * logit columns (columns of the out_V row), the compaction and sample_top_k_p (acb_sample_top_k_p)
+ * with u[a] (host) the canonical uniform of that sequence's generator. sampled[a] (host) receives
+ * the compact index: 0 for EOS, 1 + c for audio code c. Only n_active ints leave the device. */
+ACB_API acb_status acb_qw3lm_forward_batch_sample(acb_qw3lm * m, const int32_t * token_ids,
+                                                  const int32_t * kv_sets, int n_active, int use_cfg,
+                                                  float cfg_scale, int lm_offset, int lm_count, int eos_idx,
+                                                  int code_offset, int n_codes, float temperature, float top_p,
+                                                  int top_k, const float * u, int32_t * sampled);
+
 ACB_API void       acb_qw3lm_reset_kv(acb_qw3lm * m, int kv_set);            /* qw3lm_reset_kv :227 */
 ACB_API acb_status acb_qw3lm_copy_kv(acb_qw3lm * m, int src, int dst);       /* qw3lm_copy_kv :233 */
 ACB_API acb_status acb_qw3lm_build_partial_head(acb_qw3lm * m, int lm_offset); /* :290 */

@@ -1017,3 +1017,113 @@ int orc_fsq_encode_index(const float * raw6) {
     }
     return index;
 }
+
+/* ---- LM sampling (sample_top_k_p, src/sampling.h:30-133) ---- */
+
+typedef struct {
+    int   id;
+    float prob;
+} orc_tok_prob;
+
+static int cmp_desc_f32(const void * a, const void * b) {
+    float x = *(const float *) a, y = *(const float *) b;
+    return (x < y) - (x > y);
+}
+
+/* descending probability; equal probabilities by ascending id (the reference's std::sort leaves
+ * their order unspecified) */
+static int cmp_tok_prob(const void * a, const void * b) {
+    const orc_tok_prob * x = (const orc_tok_prob *) a;
+    const orc_tok_prob * y = (const orc_tok_prob *) b;
+    if (x->prob != y->prob) {
+        return x->prob > y->prob ? -1 : 1;
+    }
+    return (x->id > y->id) - (x->id < y->id);
+}
+
+/* temperature -> top_k -> top_p -> softmax -> multinomial on logits[V] (modified in place, as the
+ * reference does); u is the draw of std::uniform_real_distribution<float>(0, sum)'s canonical
+ * variate, so r = u * sum. Returns the sampled index. */
+int orc_sample_top_k_p(float * logits, int V, float temperature, float top_p, int top_k, float u) {
+    if (temperature <= 0.0f) {
+        int best = 0;
+        for (int i = 1; i < V; i++) {
+            if (logits[i] > logits[best]) {
+                best = i;
+            }
+        }
+        return best;
+    }
+    float inv_temp = 1.0f / temperature;
+    for (int i = 0; i < V; i++) {
+        logits[i] *= inv_temp;
+    }
+    if (top_k > 0 && top_k < V) {
+        float * tmp = (float *) malloc(sizeof(float) * (size_t) V);
+        memcpy(tmp, logits, sizeof(float) * (size_t) V);
+        qsort(tmp, (size_t) V, sizeof(float), cmp_desc_f32);
+        float threshold = tmp[top_k - 1];
+        free(tmp);
+        for (int i = 0; i < V; i++) {
+            if (logits[i] < threshold) {
+                logits[i] = -INFINITY;
+            }
+        }
+    }
+    if (top_p > 0.0f && top_p < 1.0f) {
+        float max_logit = -INFINITY;
+        for (int i = 0; i < V; i++) {
+            if (logits[i] > max_logit) {
+                max_logit = logits[i];
+            }
+        }
+        float sum_exp = 0.0f;
+        for (int i = 0; i < V; i++) {
+            sum_exp += expf(logits[i] - max_logit);
+        }
+        float          inv_sum = 1.0f / sum_exp;
+        float          cutoff  = max_logit - 16.0f;
+        orc_tok_prob * buf     = (orc_tok_prob *) malloc(sizeof(orc_tok_prob) * (size_t) V);
+        int            K       = 0;
+        for (int i = 0; i < V; i++) {
+            if (logits[i] >= cutoff) {
+                buf[K].id   = i;
+                buf[K].prob = expf(logits[i] - max_logit) * inv_sum;
+                K++;
+            } else {
+                logits[i] = -INFINITY;
+            }
+        }
+        if (K > 0) {
+            qsort(buf, (size_t) K, sizeof(orc_tok_prob), cmp_tok_prob);
+            float cum = 0.0f;
+            for (int i = 0; i < K; i++) {
+                if (i > 0 && cum >= top_p) {
+                    logits[buf[i].id] = -INFINITY;
+                }
+                cum += buf[i].prob;
+            }
+        }
+        free(buf);
+    }
+    float max_val = -INFINITY;
+    for (int i = 0; i < V; i++) {
+        if (logits[i] > max_val) {
+            max_val = logits[i];
+        }
+    }
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++) {
+        logits[i] = expf(logits[i] - max_val);
+        sum += logits[i];
+    }
+    float r   = u * (sum - 0.0f) + 0.0f;
+    float acc = 0.0f;
+    for (int i = 0; i < V; i++) {
+        acc += logits[i];
+        if (acc >= r) {
+            return i;
+        }
+    }
+    return 0;
+}

@@ -129,6 +129,11 @@ void orc_timestep_embedding(float t, int dim, int max_period, float * out);
 void orc_fsq_decode_index(int index, float * out6);
 int  orc_fsq_encode_index(const float * raw6);
 
+/* sample_top_k_p (src/sampling.h:30-133) on logits[V] in place; u = the canonical uniform of the
+ * reference's std::uniform_real_distribution<float>(0, sum) draw. Equal probabilities in the top_p
+ * sort are ordered by ascending id. */
+int orc_sample_top_k_p(float * logits, int V, float temperature, float top_p, int top_k, float u);
+
 /* Thread control for the CPU baseline (0 = OpenMP default). */
 void orc_set_threads(int n);
 int  orc_get_threads(void);

@@ -61,6 +61,7 @@ def lib():
             "orc_get_threads": (I, []),
             "orc_fsq_decode_index": (None, [I, P]),
             "orc_fsq_encode_index": (I, [P]),
+            "orc_sample_top_k_p": (I, [P, I, F, F, I, F]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -841,3 +842,20 @@ class OracleTok:
                                      causal=False, final_norm=True, batch=G)
         raw = _linear(t["tokenizer.quantizer.project_in.weight"], y[0::6], t["tokenizer.quantizer.project_in.bias"])
         return np.array([fsq_encode_index(r) for r in raw], dtype=np.int32), raw
+
+
+def sample_top_k_p(logits, temperature, top_p, top_k, u) -> int:
+    """sample_top_k_p (src/sampling.h:30-133) on a copy of one logits row; u the canonical uniform."""
+    x = np.array(logits, dtype=np.float32, copy=True)
+    return int(lib().orc_sample_top_k_p(_p(x), x.size, temperature, top_p, top_k, u))
+
+
+def lm_compact_cfg(lc, lu, cfg_scale, eos_idx, code_offset, n_codes):
+    """The phase-2 targeted CFG and compaction (src/pipeline-lm.cpp:474-490): [EOS, codes...] of
+    lu + cfg * (lc - lu) (every step one f32 rounding), or of lc alone when lu is None."""
+    cols = np.concatenate([[eos_idx], code_offset + np.arange(n_codes)])
+    c = np.asarray(lc, dtype=np.float32)[cols]
+    if lu is None:
+        return c
+    u = np.asarray(lu, dtype=np.float32)[cols]
+    return (u + np.float32(cfg_scale) * (c - u)).astype(np.float32)
