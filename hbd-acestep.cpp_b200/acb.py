@@ -668,6 +668,53 @@ def sample_top_k_p(logits, temperature, top_p, top_k, u=None, uncond=None, cfg_s
     return idx
 
 
+class Stork4Tables:
+    """acb_stork4_tables over numpy copies of {ms, fpa, fpb, recf} (kept alive by this object)."""
+
+    class _C(C.Structure):
+        _fields_ = [("ms", C.c_void_p), ("ms_len", C.c_int), ("fpa", C.c_void_p), ("fpb", C.c_void_p),
+                    ("recf", C.c_void_p), ("recf_len", C.c_int)]
+
+    def __init__(self, tables):
+        import numpy as np
+        self.ms = np.ascontiguousarray(tables["ms"], dtype=np.int32)
+        self.fpa = np.ascontiguousarray(tables["fpa"], dtype=np.float64)
+        self.fpb = np.ascontiguousarray(tables["fpb"], dtype=np.float64)
+        self.recf = np.ascontiguousarray(tables["recf"], dtype=np.float64)
+        self.c = Stork4Tables._C(self.ms.ctypes.data, self.ms.size, self.fpa.ctypes.data, self.fpb.ctypes.data,
+                                 self.recf.ctypes.data, self.recf.size)
+
+
+class Stork4:
+    """STORK4 solver state on device latents (acb_stork4_*, src/solvers/solver-stork.h)."""
+
+    def __init__(self, tables, n, substeps=10):
+        self.tables = Stork4Tables(tables)
+        h = C.c_void_p()
+        fn = lib().acb_stork4_create
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.c_int64, C.c_int, C.POINTER(C.c_void_p)]
+        st = fn(C.byref(self.tables.c), int(n), int(substeps), C.byref(h))
+        if st != 0:
+            raise AcbError(f"acb_stork4_create ({lib().acb_last_error().decode()})", st)
+        self.h = h
+
+    def step(self, xt, vt, t_curr, t_prev, stream=None):
+        """xt (device f32, in place) <- one STORK4 step with velocity vt (device f32)."""
+        fn = lib().acb_stork4_step
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_void_p]
+        _check("acb_stork4_step", fn(self.h, _ptr(xt), _ptr(vt), float(t_curr), float(t_prev), _stream(stream)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            fn = lib().acb_stork4_free
+            fn.restype, fn.argtypes = None, [C.c_void_p]
+            fn(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
 def fsq_decode_index(index: int):
     """fsq_decode_index (src/fsq-detok.h:18-29): flat code -> 6 floats in [-1, 1]."""
     import numpy as np
@@ -958,7 +1005,7 @@ class DiT:
 
     def generate_ex(self, noise, context, enc, schedule, guidance_scale=1.0, solver="euler", real_S=None,
                     real_enc_S=None, seeds=None, randn=None, cancel=None, context_switch=None, cover_steps=-1,
-                    enc_switch=None, real_enc_S_switch=None, dcw_scaler=0.0):
+                    enc_switch=None, real_enc_S_switch=None, dcw_scaler=0.0, stork_substeps=10):
         """acb_dit_generate_ex (dit_ggml_generate's argument list). randn(seed, n) -> n floats is
         the SDE noise source; cancel(step_count) -> bool is polled before every step. Returns
         (x0, device ms); raises AcbError with status 9 when cancelled."""
@@ -992,9 +1039,16 @@ class DiT:
             self.h, noise.ctypes.data, context.ctypes.data, enc.ctypes.data, enc.shape[1], T, N, sched.size,
             sched.ctypes.data, out.ctypes.data, float(guidance_scale), ptr(cs), int(cover_steps),
             C.cast(cb_c, C.c_void_p) if cb_c else None, None, ptr(rs), ptr(re), ptr(es), ptr(res), ptr(sd), 1,
-            float(dcw_scaler), 0.0, b"low", solver.encode() if solver else None, 10,
+            float(dcw_scaler), 0.0, b"low", solver.encode() if solver else None, int(stork_substeps),
             C.cast(cb_r, C.c_void_p) if cb_r else None, None, C.cast(C.pointer(ms), C.c_void_p)))
         return out, ms.value
+
+    def set_stork4_tables(self, tables):
+        """ROCK4 tables {ms, fpa [len][6], fpb [len][4], recf} for the "stork4" solver."""
+        t = Stork4Tables(tables)
+        fn = lib().acb_dit_set_stork4_tables
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.c_void_p]
+        _check("acb_dit_set_stork4_tables", fn(self.h, C.byref(t.c)))
 
     def generate(self, noise, context, enc, schedule, guidance_scale=1.0, solver="euler"):
         """Host arrays: noise [N, T, Oc], context [N, T, in-Oc], enc [N, enc_S, enc_hidden] ->

@@ -88,6 +88,9 @@ struct acb_dit {
     DevBuf                          noise;         // SDE: the step's fresh noise [N][T][out_ch]
     DevBuf                          vpair, xall;   // sharded: [cond, uncond] velocities; gathered x0
     std::unique_ptr<DiTRun>         job;           // the step-level job (acb_dit_job_*)
+    acb_stork4_tables               stork_tab{};   // the caller's ROCK4 tables (acb_dit_set_stork4_tables)
+    std::vector<int>                stork_ms;
+    std::vector<double>             stork_fpa, stork_fpb, stork_recf;
     std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
 
     ~acb_dit();
@@ -883,6 +886,7 @@ struct GenArgs {
     const int *     real_enc_S_switch = nullptr;
     const int64_t * seeds             = nullptr;
     int             solver            = ACB_SOLVER_EULER;
+    int             stork_substeps    = 10;
     acb_randn_fn    randn             = nullptr;
     void *          randn_data        = nullptr;
     float *         gpu_ms            = nullptr;
@@ -912,6 +916,7 @@ struct DiTRun {
     cudaStream_t s = nullptr;
     cudaEvent_t  e0 = nullptr, e1 = nullptr, done[2] = { nullptr, nullptr };
     int          steps_run = 0;
+    acb_stork4 * stork     = nullptr;  // the STORK4 state of this run (solver stork4)
 
     ~DiTRun() {
         for (cudaEvent_t e : { e0, e1, done[0], done[1] }) {
@@ -919,6 +924,7 @@ struct DiTRun {
                 cudaEventDestroy(e);
             }
         }
+        acb_stork4_free(stork);
     }
 
     const float * ctx_of(const float * c) const { return c + (size_t) track0 * T * ctx_ch; }
@@ -977,11 +983,16 @@ struct DiTRun {
 acb_status DiTRun::begin(acb_dit * model, acb_comm * c, const GenArgs & args, int t0, int nloc, int h, int pr) {
     m = model, comm = c, g = args, track0 = t0, n = nloc, half = h, peer = pr;
     const bool dpm = g.solver == ACB_SOLVER_DPM3M, sde = g.solver == ACB_SOLVER_SDE;
+    const bool stk = g.solver == ACB_SOLVER_STORK4;
     if (!m || !g.noise || !g.context || !g.enc || g.N <= 0 || g.T <= 0 || g.enc_S <= 0 || n <= 0 ||
         g.T % m->c.patch_size != 0 ||
-        (g.solver != ACB_SOLVER_EULER && g.solver != ACB_SOLVER_DPM3M && g.solver != ACB_SOLVER_SDE) ||
+        (g.solver != ACB_SOLVER_EULER && g.solver != ACB_SOLVER_DPM3M && g.solver != ACB_SOLVER_SDE && !stk) ||
         (sde && (!g.seeds || !g.randn)) || (half >= 0 && (n != 1 || !comm))) {
         return ACB_ERR_INVALID_ARG;
+    }
+    if (stk && m->stork_ms.empty()) {
+        set_last_error("the stork4 solver needs the ROCK4 tables (acb_dit_set_stork4_tables)");
+        return ACB_ERR_UNSUPPORTED;
     }
     if (cudaSetDevice(m->device) != cudaSuccess) {
         return ACB_ERR_CUDA;
@@ -1035,6 +1046,11 @@ acb_status DiTRun::begin(acb_dit * model, acb_comm * c, const GenArgs & args, in
     }
     ACB_TRY(upload_lengths());
     ACB_TRY(m->condition(s));
+    if (stk) {
+        acb_stork4_free(stork);
+        stork = nullptr;
+        ACB_TRY(acb_stork4_create(&m->stork_tab, (int64_t) n_tot, g.stork_substeps, &stork));
+    }
     fresh.assign(sde ? n_tot : 0, 0.0f);
     tv.assign(3, 0.0f);
     cudaEventCreate(&e0);
@@ -1081,7 +1097,9 @@ acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphE
             v  = m->vt.as<float>();
         }
         float * vv = const_cast<float *>(v);
-        if (st == ACB_OK && dpm && !last) {
+        if (g.solver == ACB_SOLVER_STORK4 && !last) {
+            // the STORK4 step runs after the graph (its sub step count adapts on the host)
+        } else if (st == ACB_OK && dpm && !last) {
             st = acb_dit_dpm3m(m->xt.as<float>(), vv, m->hist1.as<float>(), m->hist2.as<float>(), hist,
                                m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
         } else if (st == ACB_OK && sde && !last) {
@@ -1180,6 +1198,10 @@ acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * ho
         if (cudaGraphLaunch(eb, s) != cudaSuccess) {
             return ACB_ERR_CUDA;
         }
+    }
+    if (stork && !last) {
+        const float * v = do_cfg ? m->vt.as<float>() : m->vel.as<float>();
+        ACB_TRY(acb_stork4_step(stork, m->xt.as<float>(), v, t_curr, t_next, (acb_stream_t) s));
     }
     if (host_out && cudaMemcpyAsync(host_out, last ? m->out.p : m->xt.p, n_tot * 4, cudaMemcpyDeviceToHost, s) !=
                         cudaSuccess) {
@@ -1320,7 +1342,6 @@ extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, cons
                                           float dcw_high_scaler, const char * dcw_mode, const char * solver_name,
                                           int stork_substeps, acb_randn_fn randn, void * randn_data, float * gpu_ms) {
     (void) use_batch_cfg;   // both settings run the batched graph: HBM is not the constraint here
-    (void) stork_substeps;  // STORK is not provided (see below)
     (void) dcw_mode;
     if (dcw_scaler > 0.0f || dcw_high_scaler > 0.0f) {
         set_last_error("acb_dit_generate_ex: DCW (dwt-haar.h) is not provided by this library");
@@ -1332,8 +1353,7 @@ extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, cons
     } else if (solver_name && std::strcmp(solver_name, "sde") == 0) {
         solver = ACB_SOLVER_SDE;
     } else if (solver_name && std::strcmp(solver_name, "stork4") == 0) {
-        set_last_error("acb_dit_generate_ex: the STORK4 solver is not provided by this library");
-        return ACB_ERR_UNSUPPORTED;
+        solver = ACB_SOLVER_STORK4;
     }
     GenArgs g;
     g.noise             = noise;
@@ -1356,10 +1376,24 @@ extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, cons
     g.real_enc_S_switch = real_enc_S_switch;
     g.seeds             = seeds;
     g.solver            = solver;
+    g.stork_substeps    = stork_substeps > 0 ? stork_substeps : 10;
     g.randn             = randn;
     g.randn_data        = randn_data;
     g.gpu_ms            = gpu_ms;
     return generate_impl(m, g);
+}
+
+extern "C" acb_status acb_dit_set_stork4_tables(acb_dit * m, const acb_stork4_tables * t) {
+    if (!m || !t || !t->ms || t->ms_len <= 0 || !t->fpa || !t->fpb || !t->recf || t->recf_len <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    m->stork_ms.assign(t->ms, t->ms + t->ms_len);
+    m->stork_fpa.assign(t->fpa, t->fpa + (size_t) t->ms_len * 6);
+    m->stork_fpb.assign(t->fpb, t->fpb + (size_t) t->ms_len * 4);
+    m->stork_recf.assign(t->recf, t->recf + t->recf_len);
+    m->stork_tab = acb_stork4_tables{ m->stork_ms.data(), t->ms_len, m->stork_fpa.data(), m->stork_fpb.data(),
+                                      m->stork_recf.data(), t->recf_len };
+    return ACB_OK;
 }
 
 // ---- sharded jobs (one process per GPU) ------------------------------------------------------
@@ -1401,8 +1435,7 @@ int solver_id(const char * name, acb_status * st) {
         return ACB_SOLVER_SDE;
     }
     if (name && std::strcmp(name, "stork4") == 0) {
-        set_last_error("the STORK4 solver is not provided by this library");
-        *st = ACB_ERR_UNSUPPORTED;
+        return ACB_SOLVER_STORK4;
     }
     return ACB_SOLVER_EULER;  // solver_lookup's fallback for unknown names
 }

@@ -243,7 +243,43 @@ ACB_API acb_status acb_dit_generate(acb_dit * m, const float * noise, const floa
                                     const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                     const float * schedule, float * output, float guidance_scale, float * gpu_ms);
 /* Solvers (the registry keys of solvers/solver-registry.h:30-33: "euler", "dpm3m", "sde"). */
-enum { ACB_SOLVER_EULER = 0, ACB_SOLVER_DPM3M = 1, ACB_SOLVER_SDE = 2 };
+enum { ACB_SOLVER_EULER = 0, ACB_SOLVER_DPM3M = 1, ACB_SOLVER_SDE = 2, ACB_SOLVER_STORK4 = 3 };
+
+/* ---- STORK4 solver (replaces src/solvers/solver-stork.h) ------------------------------------- */
+
+/* The ROCK4 tables STORK4 runs on (Abdulle 2002; the reference compiles them in as STORK4_MS,
+ * STORK4_FPA, STORK4_FPB, STORK4_RECF in solver-stork4-constants.h): ms[ms_len] increasing degrees,
+ * fpa[ms_len][6] and fpb[ms_len][4] finishing coefficients, recf[recf_len] recurrence
+ * coefficients. The library keeps its own copy. */
+typedef struct {
+    const int *    ms;
+    int            ms_len;
+    const double * fpa;
+    const double * fpb;
+    const double * recf;
+    int            recf_len;
+} acb_stork4_tables;
+
+typedef struct acb_stork4 acb_stork4;
+
+/* STORK4 state for latents of n floats on the current device (solver_stork4_step,
+ * solver-stork.h:270-315; SolverState's velocity history and step index): substeps <= 0 takes the
+ * reference's 10. */
+ACB_API acb_status acb_stork4_create(const acb_stork4_tables * tables, int64_t n, int substeps, acb_stork4 ** out);
+/* One step on device buffers: xt [n] in place from vt [n] (the guided velocity) between t_curr and
+ * t_prev. Step 0 is Euler; later steps take velocity derivatives from the history (orders 2 / 1 / 0
+ * by the reference's stability guards), run the ROCK4 sub stepping (one fused pass per attempt,
+ * the sub step count halved while the result is not finite) or fall back to Euler. Synchronises
+ * `stream` (the adaptive choice is made on the host). */
+ACB_API acb_status acb_stork4_step(acb_stork4 * st, float * xt, const float * vt, float t_curr, float t_prev,
+                                   acb_stream_t stream);
+ACB_API void       acb_stork4_reset(acb_stork4 * st);
+ACB_API int        acb_stork4_step_index(const acb_stork4 * st);
+ACB_API void       acb_stork4_free(acb_stork4 * st);
+
+/* The ROCK4 tables for the "stork4" solver of acb_dit_generate_ex / acb_dit_generate_sharded /
+ * acb_dit_job_begin (copied; without them that solver returns ACB_ERR_UNSUPPORTED). */
+ACB_API acb_status acb_dit_set_stork4_tables(acb_dit * m, const acb_stork4_tables * tables);
 /* acb_dit_generate with dit_ggml_generate's solver choice (dit-sampler.h:391-398, 608-611): Euler or
  * DPM++ 3M (acb_dit_dpm3m on the velocity after guidance, its history on the device; the last
  * step is the x0 prediction for every solver). Other solver values: ACB_ERR_INVALID_ARG. */

@@ -598,7 +598,7 @@ def dit_from_gguf_tensors(cfg, tensors):
 
 def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, momentum=-0.75, norm_threshold=2.5,
                  solver="euler", real_S=None, real_enc_S=None, seeds=None, randn=None, context_switch=None,
-                 cover_steps=-1, enc_switch=None, real_enc_S_switch=None):
+                 cover_steps=-1, enc_switch=None, real_enc_S_switch=None, stork_tables=None, stork_substeps=10):
     """dit_ggml_generate (src/dit-sampler.h:132-711) over an OracleDiT with the Euler solver,
     DPM++ 3M (solver="dpm3m", solver-dpm.h:14-50) or SDE ancestral (solver="sde",
     solver-sde.h:17-38; randn(seed, n) gives the fresh noise of track b at step k from seed
@@ -617,6 +617,7 @@ def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, mo
     re = None if real_enc_S is None else np.asarray(real_enc_S, np.int32)
     re_unc = re
     switched = False
+    stork = Stork4(stork_tables, stork_substeps) if solver == "stork4" else None
     for step, t in enumerate(schedule):
         if context_switch is not None and cover_steps >= 0 and step >= cover_steps and not switched:
             switched = True
@@ -654,6 +655,9 @@ def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, mo
             return (xt - v * np.float32(t)).astype(np.float32)
         if solver == "dpm3m":
             xt, hist1, hist2 = dpm3m_step(xt, v, hist1, hist2, t, schedule[step + 1])
+            continue
+        if stork is not None:
+            xt = stork.step(xt, v, t, schedule[step + 1])
             continue
         if solver == "sde":
             fresh = np.stack([np.asarray(randn(int(seeds[b]) + step + 1, T * Oc), np.float32).reshape(T, Oc)
@@ -859,3 +863,133 @@ def lm_compact_cfg(lc, lu, cfg_scale, eos_idx, code_offset, n_codes):
         return c
     u = np.asarray(lu, dtype=np.float32)[cols]
     return (u + np.float32(cfg_scale) * (c - u)).astype(np.float32)
+
+
+class Stork4:
+    """solver_stork4_step (src/solvers/solver-stork.h:270-315) in float32 with every product and sum
+    rounded in the reference's order (d2v in float64), over the caller's ROCK4 tables
+    {ms, fpa [len][6], fpb [len][4], recf}."""
+
+    def __init__(self, tables, substeps=10):
+        self.ms = [int(v) for v in tables["ms"]]
+        self.fpa = np.asarray(tables["fpa"], np.float64).reshape(-1, 6)
+        self.fpb = np.asarray(tables["fpb"], np.float64).reshape(-1, 4)
+        self.recf = np.asarray(tables["recf"], np.float64)
+        self.substeps = substeps
+        self.step_index = 0
+        self.hist = []  # (vt, dt), newest last, at most 3
+
+    def _push(self, vt, dt):
+        self.hist.append((np.array(vt, np.float32, copy=True), np.float32(dt)))
+        self.hist = self.hist[-3:]
+
+    def _derivs(self, vt):
+        """_stork_compute_derivatives (solver-stork.h:72-127): (order, dv, d2v)."""
+        f = np.float32
+        if not self.hist:
+            return 0, None, None
+        v1, h1 = self.hist[-1]
+        if h1 == 0:
+            return 0, None, None
+        dv = ((v1 - vt) / h1).astype(np.float32)
+        n = vt.size
+        vt_rms = np.sqrt(np.sum(vt.astype(np.float64) ** 2) / n)
+        dv_rms = np.sqrt(np.sum(dv.astype(np.float64) ** 2) / n)
+        if vt_rms > 0 and dv_rms * abs(float(h1)) > 5.0 * vt_rms:
+            return 0, dv, None
+        if len(self.hist) < 2:
+            return 1, dv, None
+        v2, h2 = self.hist[-2]
+        if h2 == 0:
+            return 1, dv, None
+        h1d, h2d = float(h1), float(h2)
+        denom = h1d * h2d * (h1d + h2d)
+        if abs(denom) < 1e-30:
+            return 1, dv, None
+        coeff = 2.0 / denom
+        d2v = (coeff * ((v2.astype(np.float64) * h1d - v1.astype(np.float64) * (h1d + h2d))
+                        + vt.astype(np.float64) * h2d)).astype(np.float32)
+        d2v_rms = np.sqrt(np.sum(d2v.astype(np.float64) ** 2) / n)
+        if vt_rms > 0 and d2v_rms * float(h1) * float(h1) > 5.0 * vt_rms:
+            return 1, dv, d2v
+        return 2, dv, d2v
+
+    @staticmethod
+    def _taylor(order, diff, v, dv, d2v):
+        f = np.float32
+        if order >= 1 and dv is not None:
+            if order >= 2 and d2v is not None:
+                half = f(f(f(0.5) * diff) * diff)
+                return ((v + diff * dv) + half * d2v).astype(np.float32)
+            return (v + diff * dv).astype(np.float32)
+        return v.copy()
+
+    def _mdegr(self, s):
+        mp1 = 1
+        for i, m in enumerate(self.ms):
+            if m >= s:
+                return m, i, mp1 - 1
+            mp1 += m * 2 - 1
+        return self.ms[-1], len(self.ms) - 1, mp1 - 1
+
+    def _substep(self, xt, vt, s, t_curr, t_prev, order, dv, d2v):
+        """_rock4_substep (solver-stork.h:160-268): (x_next, finite)."""
+        with np.errstate(over="ignore", invalid="ignore"):
+            return self._substep_body(xt, vt, s, t_curr, t_prev, order, dv, d2v)
+
+    def _substep_body(self, xt, vt, s, t_curr, t_prev, order, dv, d2v):
+        f = np.float32
+        s = min(s, self.ms[-1])
+        mdeg, mz, mr = self._mdegr(s)
+        t_curr, t_prev = f(t_curr), f(t_prev)
+        dt = f(t_curr - t_prev)
+        R = self.recf
+        t1 = f(-dt * f(R[mr]))
+        ci1 = f(t_curr + t1)
+        ci2, ci3 = ci1, t_curr
+        y1 = (xt + t1 * vt).astype(np.float32)
+        y2 = xt.copy()
+        for j in range(2, mdeg + 1):
+            diff = f(ci1 - t_curr)
+            vel = self._taylor(order, diff, vt, dv, d2v)
+            temp1 = f(-dt * f(R[mr + 2 * (j - 2) + 1]))
+            temp3 = f(-f(R[mr + 2 * (j - 2) + 2]))
+            temp2 = f(f(1.0) - temp3)
+            cn = f(f(temp1 + f(temp2 * ci2)) + f(temp3 * ci3))
+            y = ((temp1 * vel + temp2 * y1) + temp3 * y2).astype(np.float32)
+            y2, y1 = y1, y
+            ci3, ci2, ci1 = ci2, cn, cn
+        A, B = self.fpa[mz], self.fpb[mz]
+        fa = [f(-dt * f(a)) for a in A]
+        fb = [f(-dt * f(b)) for b in B]
+        F1 = self._taylor(order, f(ci1 - t_curr), vt, dv, d2v)
+        F2 = self._taylor(order, f(f(ci1 + fa[0]) - t_curr), vt, dv, d2v)
+        F3 = self._taylor(order, f(f(f(ci1 + fa[1]) + fa[2]) - t_curr), vt, dv, d2v)
+        F4 = self._taylor(order, f(f(f(f(ci1 + fa[3]) + fa[4]) + fa[5]) - t_curr), vt, dv, d2v)
+        out = ((((y1 + fb[0] * F1) + fb[1] * F2) + fb[2] * F3) + fb[3] * F4).astype(np.float32)
+        return out, bool(np.all(np.isfinite(out)))
+
+    def step(self, xt, vt, t_curr, t_prev):
+        f = np.float32
+        xt = np.asarray(xt, np.float32)
+        vt = np.asarray(vt, np.float32)
+        dt = f(f(t_curr) - f(t_prev))
+        if self.step_index == 0:
+            out = (xt - vt * dt).astype(np.float32)
+            self._push(vt, dt)
+            self.step_index = 1
+            return out
+        order, dv, d2v = self._derivs(vt)
+        s = max(self.substeps, 2)
+        out = None
+        while s >= 2:
+            nxt, ok = self._substep(xt, vt, s, t_curr, t_prev, order, dv, d2v)
+            if ok:
+                out = nxt
+                break
+            s //= 2
+        if out is None:
+            out = (xt - vt * dt).astype(np.float32)
+        self._push(vt, dt)
+        self.step_index += 1
+        return out
