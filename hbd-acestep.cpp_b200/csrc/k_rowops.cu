@@ -461,6 +461,141 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     }
 }
 
+// 128-wide heads, a warp per token: the half-warps take two heads at a time, lane l16 = lane & 15
+// owning elements 8*l16 .. 8*l16 + 7 (16- or 32-byte accesses). The NeoX partner of element i < 64
+// is i + 64, eight lanes away (a shuffle), and every head of the token shares the lane's norm
+// weights and rope rows, which are loaded once per token instead of once per head. All heads'
+// loads are issued before the first reduction. Same arithmetic as qk_norm_rope_kernel: the sum of
+// squares in double (16-lane butterfly), (x * scale) * w, then the rotation.
+template <int TI, int TO>
+__global__ void __launch_bounds__(256) qk_tok_kernel(const void * __restrict__ src, int64_t sts,
+                                                     void * __restrict__ dst, int64_t dts, int64_t dhs, int64_t dps,
+                                                     int64_t n_tok, int n_heads, const float * __restrict__ w,
+                                                     float eps, const int32_t * __restrict__ pos,
+                                                     const float * __restrict__ rope, int max_pos,
+                                                     int * __restrict__ err) {
+    using ei          = typename io<TI>::t;
+    using eo          = typename io<TO>::t;
+    constexpr int D   = 128;
+    constexpr int U   = 4;  // head pairs per pass: 8 heads' loads in flight per warp
+    const int     lane = threadIdx.x & 31;
+    const int64_t t    = (int64_t) blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= n_tok) {
+        return;
+    }
+    const int  sub   = lane >> 4;
+    const int  l16   = lane & 15;
+    const bool first = l16 < 8;
+    const int  p     = pos ? __ldg(pos + t) : 0;
+    if (pos && (p < 0 || p >= max_pos)) {
+        if (lane == 0 && err) {
+            atomicOr(err, ACB_DEVERR_POS_RANGE);
+        }
+        return;
+    }
+    float wv[8];
+    if (w) {
+        ld_run<ACB_TYPE_F32, 4, true>(w + 8 * l16, wv);
+        ld_run<ACB_TYPE_F32, 4, true>(w + 8 * l16 + 4, wv + 4);
+    }
+    float cs[8], sn[8];
+    if (rope) {
+        const float * c = rope + (int64_t) p * D + 16 * (l16 & 7);  // (cos, sin) of pairs 8*(l16&7) ..
+        float         r[16];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            ld_run<ACB_TYPE_F32, 4, true>(c + 4 * q, r + 4 * q);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            cs[e] = r[2 * e];
+            sn[e] = first ? -r[2 * e + 1] : r[2 * e + 1];
+        }
+    }
+    const int npairs = (n_heads + 1) / 2;
+    for (int base = 0; base < npairs; base += U) {
+        // phase by phase over the U head pairs, so that their loads, shuffle chains, square roots
+        // and divisions overlap (pairs past the end hold zeros and store nothing)
+        float x[U][8];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int h = 2 * (base + u) + sub;
+            if (base + u < npairs && h < n_heads) {
+                const ei * s = reinterpret_cast<const ei *>(src) + t * sts + (int64_t) h * D + 8 * l16;
+                if constexpr (sizeof(ei) == 2) {
+                    ld_run<TI, 8, true>(s, x[u]);
+                } else {
+                    ld_run<TI, 4, true>(s, x[u]);
+                    ld_run<TI, 4, true>(s + 4, x[u] + 4);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    x[u][e] = 0.0f;
+                }
+            }
+        }
+        if (w) {
+            // the four heads' sums of squares by a transposed reduction over the 16 lanes: after
+            // the exchanges at distances 8 and 4 each lane holds one head's partial (head
+            // 2*bit3 + bit2 of its lane index) and finishes it with two more, so there are five
+            // double shuffles and one square root and division per lane instead of sixteen and
+            // four
+            double v[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                v[u] = 0.0;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    v[u] += (double) __fmul_rn(x[u][e], x[u][e]);
+                }
+            }
+            const bool   b8 = (lane & 8) != 0, b4 = (lane & 4) != 0;
+            const double r0 = __shfl_xor_sync(0xffffffffu, b8 ? v[0] : v[2], 8);
+            const double r1 = __shfl_xor_sync(0xffffffffu, b8 ? v[1] : v[3], 8);
+            const double w0 = (b8 ? v[2] : v[0]) + r0;
+            const double w1 = (b8 ? v[3] : v[1]) + r1;
+            double       z  = (b4 ? w1 : w0) + __shfl_xor_sync(0xffffffffu, b4 ? w0 : w1, 4);
+            z += __shfl_xor_sync(0xffffffffu, z, 2);
+            z += __shfl_xor_sync(0xffffffffu, z, 1);
+            const float mine = rms_scale_pow2<D>(z, eps);
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const float sc = __shfl_sync(0xffffffffu, mine, (lane & 19) | (u << 2));
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    x[u][e] = __fmul_rn(__fmul_rn(x[u][e], sc), wv[e]);
+                }
+            }
+        }
+        if (rope) {
+            // first half: x0*c - x1*s with x1 the partner; second half: x0*s + x1*c with x0 the
+            // partner -- both own*c + partner*s' with s' = -s in the first half (exact negation)
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const float o = __shfl_xor_sync(0xffffffffu, x[u][e], 8);
+                    x[u][e]       = __fadd_rn(__fmul_rn(x[u][e], cs[e]), __fmul_rn(o, sn[e]));
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int h = 2 * (base + u) + sub;
+            if (base + u < npairs && h < n_heads) {
+                eo * d = reinterpret_cast<eo *>(dst) + t * dts + (int64_t) h * dhs + (int64_t) p * dps + 8 * l16;
+                if constexpr (sizeof(eo) == 2) {
+                    st_run<TO, 8, true>(d, x[u]);
+                } else {
+                    st_run<TO, 4, true>(d, x[u]);
+                    st_run<TO, 4, true>(d + 4, x[u] + 4);
+                }
+            }
+        }
+    }
+}
+
 // q/k RMSNorm (+ NeoX RoPE) of 128-wide heads into exact hi/lo f16 planes: one warp per
 // (token, head); heads [0, nq) use wq, heads [nq, nq + nk) use wk. Lane l holds elements
 // (2l, 2l+1) of each half (8-byte loads), so each NeoX pair (i, i + 64) is in one lane.
@@ -573,6 +708,13 @@ static acb_status launch_qk(const void * src, int64_t sts, void * dst, int64_t d
     auto       al = [](const void * q, int b) { return (reinterpret_cast<uintptr_t>(q) % (uintptr_t) b) == 0; };
     const bool vec = E > 1 && al(src, E * si) && al(dst, E * so) && sts % E == 0 && dts % E == 0 && dhs % E == 0 &&
                      dps % E == 0 && (!w || al(w, E * 4)) && (!rope || al(rope, 2 * E * 4));
+    const bool tokv = D == 128 && al(src, 8 * si) && al(dst, 8 * so) && sts % 8 == 0 && dts % 8 == 0 &&
+                      dhs % 8 == 0 && dps % 8 == 0 && (!w || al(w, 16)) && (!rope || al(rope, 16));
+    if (tokv) {
+        qk_tok_kernel<TI, TO><<<(unsigned) ((n_tok + 7) / 8), 256, 0, st>>>(src, sts, dst, dts, dhs, dps, n_tok,
+                                                                           n_heads, w, eps, pos, rope, max_pos, err);
+        return launch_status();
+    }
     switch (D) {
         case 64:
             launch_qk_e<TI, TO, 1, 4>(false, grid, src, sts, dst, dts, dhs, dps, n_tok, n_heads, w, eps, pos, rope,
