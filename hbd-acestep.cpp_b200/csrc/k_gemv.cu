@@ -939,6 +939,149 @@ static acb_status dispatch_mp(const GemvParams & p, bool pdl, cudaStream_t st) {
     return launch_gemv<QT, 8, PRO>(p, pdl, st);
 }
 
+// ---- BF16 / F16 weights (the unquantised GGUFs convert.py writes) -------------------------------
+// ggml converts the activation to the weight's type and multiplies in f32: a bf16 x bf16 or
+// f16 x f16 product is exact in f32, so the products are added in double and rounded to f32 once
+// -- the same canonical rule as the quantised rows, independent of how a row is split. The block's
+// 512 threads first write every activation row (prologue applied, rounded to the weight type) to
+// shared memory; then each warp takes kHalfRowsPerWarp weight rows, its lanes streaming 16-byte
+// runs of 8 weights, with a double butterfly at the end of each row.
+constexpr int kHalfRowsPerWarp = 4;
+
+template <int WT, int MT, int PRO>
+__global__ void __launch_bounds__(kConsumerWarps * 32) gemv_half_kernel(const GemvParams p) {
+    extern __shared__ __align__(16) uint8_t gh_smem[];
+    using et        = typename io<WT>::t;
+    et *      xs    = reinterpret_cast<et *>(gh_smem);  // [MT][K]
+    __shared__ double red[kConsumerWarps];
+    const int tid   = threadIdx.x;
+    const int warp  = tid >> 5, lane = tid & 31;
+    ptx::grid_dep_wait();
+    const bool vec = (p.x_stride % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
+                     (p.norm_w == nullptr || (reinterpret_cast<uintptr_t>(p.norm_w) & 15) == 0);
+    for (int m = 0; m < p.M; m++) {
+        const float sc = PRO == PRO_RMSNORM ? rms_scale_block(p, m, red) : 1.0f;
+        for (int b = tid; b < p.K / 32; b += kConsumerWarps * 32) {
+            float v[32];
+            act_block32<PRO>(p, m, b * 32, sc, vec, v);
+            et * d = xs + (int64_t) m * p.K + b * 32;
+#pragma unroll
+            for (int e = 0; e < 32; e++) {
+                d[e] = io<WT>::from_f(v[e]);
+            }
+        }
+    }
+    __syncthreads();
+    const int64_t row0 = ((int64_t) blockIdx.x * kConsumerWarps + warp) * kHalfRowsPerWarp;
+    for (int r = 0; r < kHalfRowsPerWarp; r++) {
+        const int64_t n = row0 + r;
+        if (n >= p.N) {
+            break;
+        }
+        const et * wr = reinterpret_cast<const et *>(p.W + n * p.row_bytes);
+        double     acc[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            acc[m] = 0.0;
+        }
+        for (int k = lane * 8; k < p.K; k += 256) {
+            union {
+                uint4 u;
+                et    e[8];
+            } w;
+            w.u = __ldcs(reinterpret_cast<const uint4 *>(wr + k));
+            float wf[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                wf[e] = io<WT>::to_f(w.e[e]);
+            }
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                if (m < p.M) {
+                    union {
+                        uint4 u;
+                        et    e[8];
+                    } x;
+                    x.u = *reinterpret_cast<const uint4 *>(xs + (int64_t) m * p.K + k);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        acc[m] += (double) __fmul_rn(wf[e], io<WT>::to_f(x.e[e]));
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            acc[m] = warp_sum(acc[m]);
+        }
+        if (lane == 0) {
+            for (int m = 0; m < p.M; m++) {
+                float v = (float) acc[m];
+                if (p.epilogue == EPI_ADD) {
+                    v = __fadd_rn(p.res[(int64_t) m * p.res_stride + n], v);
+                }
+                p.y[(int64_t) m * p.y_stride + n] = v;
+            }
+        }
+    }
+    ptx::grid_dep_launch();
+}
+
+template <int WT, int MT, int PRO>
+static acb_status launch_half(const GemvParams & p, bool pdl, cudaStream_t st) {
+    const size_t smem = (size_t) p.M * p.K * 2;
+    auto         kern = gemv_half_kernel<WT, MT, PRO>;
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem) !=
+                                cudaSuccess) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const int64_t rows_per_cta = (int64_t) kConsumerWarps * kHalfRowsPerWarp;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) ((p.N + rows_per_cta - 1) / rows_per_cta));
+    cfg.blockDim           = dim3(kConsumerWarps * 32);
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = pdl ? attr : nullptr;
+    cfg.numAttrs                                       = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return ACB_ERR_CUDA;
+    }
+    return ACB_OK;
+}
+
+template <int WT, int PRO>
+static acb_status dispatch_half_mp(const GemvParams & p, bool pdl, cudaStream_t st) {
+    if (p.M <= 1) {
+        return launch_half<WT, 1, PRO>(p, pdl, st);
+    }
+    if (p.M <= 2) {
+        return launch_half<WT, 2, PRO>(p, pdl, st);
+    }
+    if (p.M <= 4) {
+        return launch_half<WT, 4, PRO>(p, pdl, st);
+    }
+    return launch_half<WT, 8, PRO>(p, pdl, st);
+}
+
+template <int WT>
+static acb_status dispatch_half(const GemvParams & p, bool pdl, cudaStream_t st) {
+    switch (p.prologue) {
+        case PRO_RMSNORM:
+            return dispatch_half_mp<WT, PRO_RMSNORM>(p, pdl, st);
+        case PRO_SUM_SPLITS:
+            return dispatch_half_mp<WT, PRO_SUM_SPLITS>(p, pdl, st);
+        case PRO_SWIGLU:
+            return dispatch_half_mp<WT, PRO_SWIGLU>(p, pdl, st);
+        default:
+            return dispatch_half_mp<WT, PRO_X>(p, pdl, st);
+    }
+}
+
 template <int QT>
 static acb_status dispatch_m(const GemvParams & p, bool pdl, cudaStream_t st) {
     switch (p.prologue) {
@@ -1017,6 +1160,14 @@ extern "C" acb_status acb_gemv(const void * W, int w_type, int64_t N, int64_t K,
             }
             p.row_bytes = K / 256 * 210;
             return dispatch_m<ACB_TYPE_Q6_K>(p, pdl, st);
+        case ACB_TYPE_BF16:
+        case ACB_TYPE_F16:
+            if (K % 256 != 0 || (size_t) M * K * 2 > 200 * 1024) {
+                return ACB_ERR_UNSUPPORTED;
+            }
+            p.row_bytes = K * 2;
+            return w_type == ACB_TYPE_BF16 ? dispatch_half<ACB_TYPE_BF16>(p, pdl, st)
+                                           : dispatch_half<ACB_TYPE_F16>(p, pdl, st);
         default:
             return ACB_ERR_UNSUPPORTED;
     }

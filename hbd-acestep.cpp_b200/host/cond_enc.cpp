@@ -96,7 +96,7 @@ struct Linears {
                 }
             }
         }
-        if (xq.alloc((size_t) n * 3 * kmax * 2, false) != ACB_OK || ws.alloc(wsb, false) != ACB_OK) {
+        if (xq.alloc((size_t) n * 3 * kmax * 2, false) != ACB_OK || ws.alloc(wsb, true) != ACB_OK) {  // zeroed split-K tickets
             cap = 0;
             set_last_error("linear scratch allocation failed");
             return ACB_ERR_OOM;

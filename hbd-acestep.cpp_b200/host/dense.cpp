@@ -1,6 +1,8 @@
 // dense.cpp -- tensor-core linears with the reference's quantised mul_mat arithmetic.
 #include "dense.h"
 
+#include <cstdlib>
+
 #include "host_common.h"
 
 namespace acb {
@@ -17,6 +19,21 @@ size_t DenseLinear::elems(const std::vector<DevTensor *> & parts) {
         n += (size_t) t->N * (size_t) t->K;
     }
     return parts.empty() ? 0 : n * (splits_weights(acb_vec_dot_type(parts[0]->type)) ? 3 : 1);
+}
+
+static int env_rows(const char * name, int fallback) {
+    const char * e = std::getenv(name);
+    return e && *e ? std::atoi(e) : fallback;
+}
+
+int qkv_fuse_min_rows() {
+    static const int v = env_rows("ACB_QKV_FUSE_MIN_ROWS", 1024);
+    return v;
+}
+
+int ffn_fuse_min_rows() {
+    static const int v = env_rows("ACB_FFN_FUSE_MIN_ROWS", 1024);
+    return v;
 }
 
 acb_status dense_build(DenseLinear & L, const std::vector<DevTensor *> & parts, uint16_t * dst, const int32_t * ids,
@@ -121,7 +138,7 @@ acb_status dense_ffn(const DenseLinear & Lgu, const DenseLinear & Ldown, bool ex
     const int64_t F         = Ldown.K;
     const bool    down3     = exact && Ldown.split;
     const int     vt        = Ldown.vec;
-    const bool    fusable   = Lgu.N == 2 * F && F % 128 == 0 && M >= kFfnFuseMinRows &&
+    const bool    fusable   = Lgu.N == 2 * F && F % 128 == 0 && M >= ffn_fuse_min_rows() &&
                          (vt == ACB_TYPE_Q8_0 || vt == ACB_TYPE_F16 || vt == ACB_TYPE_BF16) &&
                          Lgu.op == Ldown.op;
     if (!fusable) {

@@ -87,12 +87,14 @@ acb_status dense_forward_operand(const DenseLinear & L, bool exact, int M, void 
                                  cudaStream_t st);
 
 // Rows from which the q/k/v projection runs with the QKV epilogue (acb_gemm_qkv_planes; fewer rows
-// take the split-K GEMM and the separate norm / transpose passes).
-constexpr int kQkvFuseMinRows = 1024;
+// take the split-K GEMM and the separate norm / transpose passes). ACB_QKV_FUSE_MIN_ROWS in the
+// environment (read once) overrides the default.
+int qkv_fuse_min_rows();
 
 // Rows from which the feed-forward block runs its gate/up GEMM with the SwiGLU epilogue (the
 // fused form needs whole waves of 256-row tiles to pay off; fewer rows take the split-K path).
-constexpr int kFfnFuseMinRows = 1024;
+// ACB_FFN_FUSE_MIN_ROWS overrides the default.
+int ffn_fuse_min_rows();
 
 // Feed-forward block out = epi(down(swiglu(gate_up(x)))) (ggml_swiglu between the two
 // projections, src/dit-graph.h:259-268, src/qwen3-enc.h:217-223): x f32 [M][xs] (normalised

@@ -199,7 +199,7 @@ acb_status acb_dit::reserve(int Ng_, int T, int enc_S_) {
                 }
             }
         }
-        A(ws, wsb);
+        A(ws, wsb, true);  // the split-K ticket area starts at zero
     }
     // positions 0..S-1 per sequence and the rope table
     {
@@ -323,7 +323,7 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ns_sa.scale           = scale_sa;
     ns_sa.shift           = shift_sa;
     ns_sa.rows_per_sample = R;
-    if (Nh % 2 == 0 && Nkv % 2 == 0 && R >= kQkvFuseMinRows) {
+    if (Nh % 2 == 0 && Nkv % 2 == 0 && R >= qkv_fuse_min_rows()) {
         // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue: the hi (and,
         // exact, lo) planes of Q||K and of V^T for the tensor-core attention
         const int64_t W  = QD + KD;
@@ -384,7 +384,7 @@ acb_status acb_dit::layer(int l, cudaStream_t s) {
     ns_ca.eps = eps;
     // the query's RMSNorm (q_norm) into the attention operand planes: in the q projection's epilogue
     // (from 1024 rows), else through f32
-    const bool cq_fused = Nh % 2 == 0 && R >= kQkvFuseMinRows;
+    const bool cq_fused = Nh % 2 == 0 && R >= qkv_fuse_min_rows();
     float *    cq       = qkv32.as<float>();
     if (cq_fused) {
         int64_t Kp = 0;

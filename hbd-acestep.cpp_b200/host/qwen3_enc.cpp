@@ -152,7 +152,7 @@ acb_status acb_qwen3_enc::reserve(int R, int S, int per) {
                                  acb_gemm_workspace_bytes(M, H, km * F) });
             }
         }
-        bad |= ws.alloc(wsb, false) != ACB_OK;
+        bad |= ws.alloc(wsb, true) != ACB_OK;  // the split-K ticket area starts at zero
     }
     if (!err.p) {
         bad |= err.alloc(4) != ACB_OK;
@@ -209,7 +209,7 @@ acb_status acb_qwen3_enc::enqueue_layers(int B, int S, int l0, int l1, cudaStrea
         NormSpec ns_in;
         ns_in.w   = (const float *) L.attn_norm->data;
         ns_in.eps = eps;
-        if (Nh % 2 == 0 && Nkv % 2 == 0 && R >= kQkvFuseMinRows) {
+        if (Nh % 2 == 0 && Nkv % 2 == 0 && R >= qkv_fuse_min_rows()) {
             // qkv projection with q/k RMSNorm + RoPE and the V transpose in its epilogue
             const int64_t W  = QD + KD;
             const int64_t lo = exact ? (int64_t) cap * W : 0;
