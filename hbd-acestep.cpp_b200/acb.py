@@ -149,6 +149,8 @@ def lib():
                                         I, P, P]),
             "acb_gemm_pair_clusters": (I, [I]),
             "acb_sample_work_bytes": (C.c_size_t, [I, I]),
+            "acb_lora_delta_add": (I, [P, I64, I64, P, P, I, F, P]),
+            "acb_requant": (I, [P, I64, I64, I, P, P]),
             "acb_sample_top_k_p": (I, [P, I64, P, I64, F, I, I64, I, I, F, F, I, P, P, P, P]),
             "acb_fsq_project_out": (I, [P, I, P, I, I, P, P, I64, P, P]),
             "acb_fsq_quantize": (I, [P, I64, P, I, P, P]),
@@ -938,13 +940,15 @@ class DiT:
               "out_channels", "patch_size", "sliding_window", "rope_theta", "rms_norm_eps", "enc_hidden_size",
               "has_null_condition"]
 
-    def __init__(self, gguf_path: str, device: int = 0):
+    def __init__(self, gguf_path: str, device: int = 0, adapter: str | None = None, adapter_scale: float = 1.0):
         import numpy as np
         self.np = np
         h = C.c_void_p()
-        st = lib().acb_dit_load(gguf_path.encode(), device, C.byref(h))
+        fn = lib().acb_dit_load_ex
+        fn.restype, fn.argtypes = C.c_int, [C.c_char_p, C.c_int, C.c_char_p, C.c_float, C.POINTER(C.c_void_p)]
+        st = fn(gguf_path.encode(), device, adapter.encode() if adapter else None, float(adapter_scale), C.byref(h))
         if st != 0:
-            raise AcbError(f"acb_dit_load ({lib().acb_last_error().decode()})", st)
+            raise AcbError(f"acb_dit_load_ex ({lib().acb_last_error().decode()})", st)
         self.h = h
 
         class Cfg(C.Structure):

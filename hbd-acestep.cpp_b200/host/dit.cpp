@@ -29,6 +29,7 @@
 
 #include "../../include/acb_models.h"
 #include "comm.h"
+#include "adapter.h"
 #include "dense.h"
 #include "gguf.h"
 #include "host_common.h"
@@ -521,6 +522,11 @@ bool conv_to_f32(const GGUFFile & gf, const std::string & name, int H, int ch, i
 }  // namespace
 
 extern "C" acb_status acb_dit_load(const char * gguf_path, int device, acb_dit ** out) {
+    return acb_dit_load_ex(gguf_path, device, nullptr, 1.0f, out);
+}
+
+extern "C" acb_status acb_dit_load_ex(const char * gguf_path, int device, const char * adapter_path,
+                                      float adapter_scale, acb_dit ** out) {
     if (!gguf_path || !out) {
         return ACB_ERR_INVALID_ARG;
     }
@@ -660,6 +666,15 @@ extern "C" acb_status acb_dit_load(const char * gguf_path, int device, acb_dit *
     }
     ACB_TRY(A.upload(m->st));
     ACB_TRY(stage->upload(m->st));
+    if (adapter_path) {
+        // LoRA merged into the staged decoder weights before their resident copies exist
+        int merged = 0;
+        const acb_status as = adapter_merge(adapter_path, adapter_scale, *stage, m->st, &merged);
+        if (as != ACB_OK) {
+            const std::string why = acb_last_error();
+            return bad(as, why);
+        }
+    }
 
     // proj_out bias repeated over the patch positions (ggml_add broadcast of [out_ch] over out_ch*P)
     {

@@ -31,6 +31,16 @@ inline float host_bf16_to_f32(uint16_t h) {
     return f;
 }
 
+// float to bfloat16, round to nearest even (NaN kept a quiet NaN), as ggml_fp32_to_bf16 does
+inline uint16_t host_f32_to_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) {
+        return (uint16_t) ((u >> 16) | 64);
+    }
+    return (uint16_t) ((u + (0x7fffu + ((u >> 16) & 1u))) >> 16);
+}
+
 inline float host_f16_to_f32(uint16_t h) {
     const uint32_t sign = (uint32_t) (h & 0x8000) << 16;
     const uint32_t exp  = (h >> 10) & 0x1f;

@@ -42,7 +42,13 @@ DevTensor * WeightArena::try_load(const GGUFFile & gf, const std::string & name)
     dims_kn(s, K, N);
     DevTensor * t = reserve(s->type, K, N, s->nbytes);
     pending_.push_back({ t, s->data, s->nbytes, 0 });
+    by_name_[name] = t;
     return t;
+}
+
+DevTensor * WeightArena::get(const std::string & name) const {
+    const auto it = by_name_.find(name);
+    return it == by_name_.end() ? nullptr : it->second;
 }
 
 DevTensor * WeightArena::load(const GGUFFile & gf, const std::string & name) {
@@ -76,6 +82,7 @@ DevTensor * WeightArena::load_f32(const GGUFFile & gf, const std::string & name)
     DevTensor * t = reserve(ACB_TYPE_F32, K, N, n * 4);
     pending_.push_back({ t, buf.get(), n * 4, 0 });
     staging_.push_back(std::move(buf));
+    by_name_[name] = t;
     return t;
 }
 

@@ -11,6 +11,7 @@
 #include <deque>
 #include <memory>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/acb.h"
@@ -43,6 +44,8 @@ class WeightArena {
     DevTensor * load_fused(const GGUFFile & gf, const std::vector<std::string> & names);
     // A host-provided tensor (e.g. a constant).
     DevTensor * add_host(int type, int64_t K, int64_t N, const void * src, size_t nbytes);
+    // The tensor loaded under a GGUF name (load / try_load / load_f32), or nullptr.
+    DevTensor * get(const std::string & name) const;
 
     // wctx_alloc: one cudaMalloc and every pending upload.
     acb_status upload(cudaStream_t st);
@@ -61,6 +64,7 @@ class WeightArena {
     DevTensor * reserve(int type, int64_t K, int64_t N, size_t nbytes);
 
     std::deque<DevTensor>                 tensors_;
+    std::unordered_map<std::string, DevTensor *> by_name_;
     std::vector<Pending>                  pending_;
     std::vector<std::unique_ptr<float[]>> staging_;
     size_t                                total_ = 0;

@@ -153,6 +153,16 @@ ACB_API acb_status acb_get_rows(const void * table, int table_type, int64_t n_ro
  * on device (the reference requantises on the host in src/adapter-merge.h:357-472). */
 ACB_API acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int type, void * dst, acb_stream_t stream);
 
+/* LoRA delta (src/adapter-merge.h:482-672, PEFT merge_and_unload): w[n][k] += bf16(scaling *
+ * sum_r B[n][r] * A[r][k]) on f32 rows w [N][K] (the dequantised base), A [rank][K] and B [N][rank]
+ * f32 already rounded to bf16 (so each product is exact); the products are added in double and
+ * rounded to f32 once, multiplied by scaling, rounded to bf16 and added. rank <= 1024. */
+ACB_API acb_status acb_lora_delta_add(float * w, int64_t N, int64_t K, const float * A, const float * B, int rank,
+                                      float scaling, acb_stream_t stream);
+/* f32 rows back into a GGUF type: Q8_0 / Q4_K / Q6_K (acb_quantize), BF16 / F16 (nearest even), F32
+ * (copy). The requantisation step of the adapter merge. */
+ACB_API acb_status acb_requant(const float * x, int64_t rows, int64_t K, int type, void * dst, acb_stream_t stream);
+
 /* ---- dense path (configs 1, 4, 5): tensor-core GEMM ---------------------------------------- */
 
 enum {

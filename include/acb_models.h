@@ -201,6 +201,15 @@ typedef struct {
  * load, every linear dequantised once to a resident 16-bit copy ([hi|lo|hi] f16 for quantised and
  * F32 weights, see acb_act_quant_ex) for the tensor-core GEMM. */
 ACB_API acb_status acb_dit_load(const char * gguf_path, int device, acb_dit ** out);
+/* dit_ggml_load with an adapter (dit.h:421-428, adapter_merge): the LoRA at adapter_path (a PEFT
+ * directory with adapter_model.safetensors and adapter_config.json, or one safetensors file) is
+ * merged into the decoder weights at load with user scale adapter_scale, before the resident
+ * copies are built: base dequantised, + bf16(alpha/rank * scale * B.A), requantised to its GGUF
+ * type on the device (Q8_0 with ggml's quantiser; Q4_K / Q6_K with this library's encoders, which
+ * choose their scales differently from ggml's search). adapter_path NULL is acb_dit_load. A LoKr
+ * payload returns ACB_ERR_UNSUPPORTED. */
+ACB_API acb_status acb_dit_load_ex(const char * gguf_path, int device, const char * adapter_path,
+                                   float adapter_scale, acb_dit ** out);
 ACB_API acb_status acb_dit_get_config(const acb_dit * m, acb_dit_config * cfg);
 ACB_API size_t     acb_dit_weight_bytes(const acb_dit * m);
 /* exact (default, nonzero): hi/lo split products, tracking the reference CPU build to fp32

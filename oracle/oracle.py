@@ -993,3 +993,35 @@ class Stork4:
         self._push(vt, dt)
         self.step_index += 1
         return out
+
+
+# ---- LoRA merge (src/adapter-merge.h:482-672) --------------------------------------------------
+
+def lora_scaling(alpha, rank, scale) -> np.float32:
+    """(alpha / rank) * scale in f32, as adapter_merge_lora computes it."""
+    f = np.float32
+    return f(f(f(alpha) / f(rank)) * f(scale))
+
+
+def lora_merge(entry, A, B, scaling):
+    """One tensor of adapter_merge_lora: entry (qtype, raw, K, shape) -> (qtype, merged raw [N][row
+    bytes or K], merged f32 [N][K]). A [rank][K], B [N][rank] are rounded to bf16 (PEFT); the delta
+    B.A is formed from those exact products in double, rounded to f32, scaled, rounded to bf16 and
+    added to the dequantised base; the sum is requantised to the base type."""
+    qt, raw, K, shape = entry
+    N = int(np.prod(shape)) // K
+    base = _f32_of(entry).reshape(N, K)
+    a = round_bf16(np.asarray(A, np.float32)).astype(np.float64)
+    b = round_bf16(np.asarray(B, np.float32)).astype(np.float64)
+    d = (b @ a).astype(np.float32)
+    d = round_bf16((d * np.float32(scaling)).astype(np.float32))
+    merged = (base + d).astype(np.float32)
+    if qt == F32:
+        out = merged
+    elif qt == BF16:
+        out = f32_to_bf16_bits(merged)
+    elif qt == F16:
+        out = merged.astype(np.float16).view(np.uint16)
+    else:
+        out = quantize(merged, qt)
+    return qt, out, merged
