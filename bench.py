@@ -495,6 +495,12 @@ def run_ours(args):
             print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands (Q8_0-quantised activations)")),
                   flush=True)
         return
+    if args.workloads == "vae":
+        r = run_vae(dev, rank, want_cpu=not args.no_cpu_baseline)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands, f32 accumulation")),
+                  flush=True)
+        return
     if args.workloads == "enc":
         r = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
         if rank == 0:
@@ -533,6 +539,9 @@ def run_ours(args):
             if "enc" in wl:
                 torch.cuda.empty_cache()
                 line["text_encoder"] = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
+            if "vae" in wl:
+                torch.cuda.empty_cache()
+                line["vae_decode"] = run_vae(dev, rank, want_cpu=not args.no_cpu_baseline)
         if "lm5" in wl:
             # config 5's LM shards one sequence per GPU: run at every N (all ranks take part)
             torch.cuda.empty_cache()
@@ -1131,6 +1140,97 @@ def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
     return res
 
 
+VAE_T = 750  # latent frames: 30 s of 48 kHz stereo audio (1920 samples per frame)
+
+
+def vae_flops(vcfg, T) -> int:
+    """Multiply-adds x 2 of the decoder's convolutions for T latent frames (src/vae.h:353-388)."""
+    fl = 2 * T * vcfg["c0"] * 7 * vcfg["latent"]
+    t = T
+    for ic, oc, s in zip(vcfg["in_ch"], vcfg["out_ch"], vcfg["strides"]):
+        fl += 2 * t * ic * 2 * s * oc  # ConvTranspose (GEMM into 2s columns per input step)
+        t *= s
+        fl += 3 * 2 * t * (7 * oc * oc + oc * oc)  # res units: k7 conv + k1 conv
+    return fl + 2 * t * 2 * 7 * vcfg["out_ch"][-1]
+
+
+def run_vae(dev, rank, want_cpu=True, T=VAE_T, reps=10):
+    """The VAE decoder (the shipped AutoencoderOobleck shape, BF16 GGUF, random weights) on 30 s of
+    audio: device-resident timing, and the pipeline's host call (vae_ggml_decode_tiled with its
+    default chunk 1024 / overlap 64: one window at 750 frames) end to end."""
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+    import synthetic
+
+    vcfg = dict(synthetic.ACESTEP_VAE)
+    path = os.path.join(tempfile.gettempdir(), f"acb_bench_vae_r{rank}.gguf")
+    keep = {} if want_cpu else None
+    synthetic.write_vae_gguf(path, vcfg, seed=4, keep=keep)
+    vae = acb.VAE(path, device=dev.index or 0)
+    os.remove(path)
+    lat = np.random.default_rng(5).standard_normal((T, vcfg["latent"])).astype(np.float32)
+    d_lat = torch.from_numpy(lat).to(dev)
+    d_out = torch.empty((2, T * vae.up), dtype=torch.float32, device=dev)
+    for _ in range(3):
+        vae.decode_device(d_lat, d_out)
+    torch.cuda.synchronize()
+    # activations of 0.7-2.6 GB per layer at the last block: every pass streams them from HBM
+    ms_all = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        vae.decode_device(d_lat, d_out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_all.append(e0.elapsed_time(e1))
+    ms = float(np.median(ms_all))
+    audio_s = T * vae.up / 48000.0
+    out = vae.decode_tiled(lat, chunk_size=1024, overlap=64)
+    t0 = time.perf_counter()
+    e2e_n = 5
+    for _ in range(e2e_n):
+        out = vae.decode_tiled(lat, chunk_size=1024, overlap=64)
+    e2e_s = (time.perf_counter() - t0) / e2e_n
+    fl = vae_flops(vcfg, T)
+    peaks, kind = measured_peaks()
+    res = {
+        "metric": "VAE decode throughput (audio seconds per second; AutoencoderOobleck, 30 s of 48 kHz stereo)",
+        "value": round(audio_s / (ms * 1e-3), 1), "unit": "audio_s/s", "higher_is_better": True,
+        "ms_per_decode": round(ms, 3),
+        "config": {"workload": "vae_decode_30s", "latent_frames": T, "audio_samples": T * vae.up,
+                   "channels": [vcfg["c0"]] + vcfg["out_ch"], "strides": vcfg["strides"],
+                   "weights": "BF16 in the GGUF, weight-norm fused at load into f16 (as the reference)"},
+        "roofline": {"kernel": "whole decode (tcgen05 implicit-GEMM convs dominate)", "bound": "tensor",
+                     "achieved": round(fl / (ms * 1e-3) / 1e12, 1), "peak": peaks["bf16_tflops"],
+                     "peak_kind": kind, "unit": "TFLOP/s",
+                     "frac": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+                     "flops_per_decode": fl, "traffic": None},
+        "e2e": {"value": round(audio_s / e2e_s, 1), "unit": "audio_s/s", "h2d_bytes_per_step": lat.nbytes,
+                "d2h_bytes_per_step": int(out.nbytes), "path": "acb_vae_decode_tiled (chunk 1024, overlap 64)"},
+        "gpu_launches_per_decode": 2 + 5 * (3 + 3 * 4) + 1,
+    }
+    if want_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        ov = O.OracleVAE(keep)
+        n = 3  # bounded sample: 3 latent frames (0.12 s of audio)
+        t0 = time.perf_counter()
+        ref = ov.decode(lat[:n])
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": round(n * vae.up / 48000.0 / dt, 4), "unit": "audio_s/s",
+                               "cores": O.get_threads(), "kind": "port",
+                               "sample": "oracle decode of the first 3 latent frames, same weights"}
+        got = vae.decode(lat[:n])
+        res["parity_vs_oracle"] = {"cosine": round(float((got.ravel().astype(np.float64) @ ref.ravel()) /
+                                                         (np.linalg.norm(got) * np.linalg.norm(ref))), 8)}
+    vae.close()
+    return res
+
+
 DIT_TRACKS, DIT_T, DIT_ENC_S, DIT_STEPS, DIT_GUIDANCE = 4, 1500, 512, 8, 3.0
 
 
@@ -1627,12 +1727,13 @@ def main():
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
     ap.add_argument("--lm5-gen", type=int, default=LM5_GEN, help="config 5 LM tokens (profiling runs use fewer)")
-    ap.add_argument("--workloads", default="dit,ops,lm,enc,lm5,dit5",
+    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,lm5,dit5",
                     help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
-                         "decode), enc (config 1 text encoder) -- those three at N=1 as sub-results -- and lm5 "
+                         "decode), enc (config 1 text encoder), vae (the audio decoder on 30 s) -- those four at "
+                         "N=1 as sub-results -- and lm5 "
                          "(config 5's 4B Q4_K_M LM, one sequence per GPU, at every N), dit5 (config 5's DiT leg, "
                          "track pairs per GPU, at every N); without dit, ops is the "
-                         "headline; or one of gemv / gemm / enc / ditmodes / lm5 alone")
+                         "headline; or one of gemv / gemm / enc / vae / ditmodes / lm5 alone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

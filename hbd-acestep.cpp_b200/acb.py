@@ -144,6 +144,10 @@ def lib():
             "acb_act_quant_swiglu": (I, [P, I64, I64, I64, I64, I, P, I, I64, P]),
             "acb_vec_dot_type": (I, [I]),
             "acb_gemm_workspace_bytes": (C.c_size_t, [I64, I64, I64]),
+            "acb_conv1d_tc": (I, [P, I64, I64, I, P, I64, I, I, I, P, I, I64, P, P, I64, I, P, C.c_size_t, P, P]),
+            "acb_vae_snake_f16": (I, [P, I64, I64, I, P, P, P, I64, P]),
+            "acb_vae_col2im": (I, [P, I64, I, I, I, I, P, P, P]),
+            "acb_vae_out_conv": (I, [P, I64, I, P, P, P, P, P]),
             "acb_gemm_swiglu_quant": (I, [P, I64, P, I64, I64, I64, I64, P, I, I, P, I, I64, I, P, P]),
             "acb_gemm_qkv_planes": (I, [P, I64, P, I64, I64, I64, I, I, P, P, F, P, P, I, I64, P, I64, I64, P, I64, I64,
                                         I, P, P]),
@@ -612,7 +616,10 @@ class Qwen3Encoder:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
 
     def weight_bytes(self) -> int:
         return lib().acb_qwen3_weight_bytes(self.h)
@@ -714,7 +721,75 @@ class Stork4:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
+
+
+class VAE:
+    """AutoencoderOobleck decoder (acb_models.h): vae_ggml_load / vae_ggml_decode(_tiled) of src/vae.h."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        h = C.c_void_p()
+        fn = lib().acb_vae_load
+        fn.restype, fn.argtypes = C.c_int, [C.c_char_p, C.c_int, C.POINTER(C.c_void_p)]
+        st = fn(gguf_path.encode(), device, C.byref(h))
+        if st != 0:
+            raise AcbError(f"acb_vae_load ({lib().acb_last_error().decode()})", st)
+        self.h = h
+        up = lib().acb_vae_upsample
+        up.restype, up.argtypes = C.c_int, [C.c_void_p]
+        self.up = up(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            fn = lib().acb_vae_free
+            fn.restype, fn.argtypes = None, [C.c_void_p]
+            fn(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
+
+    def decode(self, latent):
+        """Host latent [T][64] -> host audio [2][T * upsample]."""
+        import numpy as np
+        x = np.ascontiguousarray(latent, dtype=np.float32)
+        T = x.shape[0]
+        out = np.empty(2 * T * self.up, dtype=np.float32)
+        n = C.c_int(0)
+        fn = lib().acb_vae_decode
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_int)]
+        _check("acb_vae_decode", fn(self.h, x.ctypes.data, T, out.ctypes.data, T * self.up, C.byref(n)))
+        return out.reshape(2, n.value)
+
+    def decode_tiled(self, latent, chunk_size=256, overlap=64, cancel=None):
+        """vae_ggml_decode_tiled: cancel() is asked before each tile; True stops with ACB_ERR_CANCELLED."""
+        import numpy as np
+        x = np.ascontiguousarray(latent, dtype=np.float32)
+        T = x.shape[0]
+        mx = T * self.up
+        out = np.empty(2 * mx, dtype=np.float32)
+        n = C.c_int(0)
+        CANCEL = C.CFUNCTYPE(C.c_int, C.c_void_p)
+        cb = CANCEL(lambda _d: 1 if cancel() else 0) if cancel is not None else CANCEL()  # CANCEL(): null
+        fn = lib().acb_vae_decode_tiled
+        fn.restype = C.c_int
+        fn.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int, CANCEL,
+                       C.c_void_p, C.POINTER(C.c_int)]
+        _check("acb_vae_decode_tiled", fn(self.h, x.ctypes.data, T, out.ctypes.data, mx, chunk_size, overlap, cb,
+                                          None, C.byref(n)))
+        return out[:2 * n.value].reshape(2, n.value)
+
+    def decode_device(self, latent, audio, stream=None):
+        fn = lib().acb_vae_decode_device
+        fn.restype, fn.argtypes = C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+        _check("acb_vae_decode_device", fn(self.h, _ptr(latent), latent.shape[0], _ptr(audio), _stream(stream)))
+        return audio
 
 
 def fsq_decode_index(index: int):
@@ -763,7 +838,10 @@ class CondEncoder:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
 
     def set_exact(self, exact: bool):
         _check("acb_cond_set_exact", lib().acb_cond_set_exact(self.h, int(bool(exact))))
@@ -813,7 +891,10 @@ class Detokenizer:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
 
     def set_exact(self, exact: bool):
         _check("acb_detok_set_exact", lib().acb_detok_set_exact(self.h, int(bool(exact))))
@@ -844,7 +925,10 @@ class Tokenizer:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
 
     def set_exact(self, exact: bool):
         _check("acb_tok_set_exact", lib().acb_tok_set_exact(self.h, int(bool(exact))))
@@ -965,7 +1049,10 @@ class DiT:
             self.h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except (TypeError, AttributeError):  # module globals already torn down at interpreter exit
+            pass
 
     def weight_bytes(self) -> int:
         return lib().acb_dit_weight_bytes(self.h)

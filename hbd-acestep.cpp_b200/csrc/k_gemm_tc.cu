@@ -87,7 +87,22 @@ struct GemmArgs {
     int           splits;  // split-K factor; > 1: raw partials to ws, epilogue by splitk_reduce_kernel
     int           kps;     // k-tiles per split
     float *       ws;      // [splits][M][N] f32 partial accumulators
+    // implicit 1-D convolution (conv_c != 0): A's tensor map covers the activation [M][conv_c] and
+    // k-tile kt reads tap (kt*64) / conv_c, channels (kt*64) % conv_c of rows m + tap*conv_dil -
+    // conv_pad (rows outside [0, M) arrive as zeros from the TMA bounds fill)
+    int           conv_c, conv_dil, conv_pad;
 };
+
+// A's coordinates of k-tile kt for a tile starting at row ma (plain GEMM or implicit convolution)
+__device__ __forceinline__ void a_coords(const GemmArgs & g, int kt, int ma, int & x, int & y) {
+    x = kt * kBK;
+    y = ma;
+    if (g.conv_c) {
+        const int tap = x / g.conv_c;
+        x -= tap * g.conv_c;
+        y += tap * g.conv_dil - g.conv_pad;
+    }
+}
 
 // up to 4 consecutive columns of one row: one vector access when all 4 are in range and aligned.
 // Values travel in a float4 and every index is static, so nothing is placed in local memory.
@@ -489,16 +504,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         break;
                     }
                     uint8_t * st = ring + (size_t) s * Cf::kStage;
+                    int       ax, ay;
+                    a_coords(g, kt, ma, ax, ay);
                     if constexpr (PAIR) {
                         const uint32_t fb = mapa_shared(ptx::smem_u32(&full[s]), 0);
                         if (leader) {
                             ptx::mbar_arrive_expect_tx(&full[s], Cf::kTx);
                         }
-                        tma_load_2d_pair(st, &tmA, kt * kBK, ma, fb);
+                        tma_load_2d_pair(st, &tmA, ax, ay, fb);
                         tma_load_2d_pair(st + Cf::kATile, &tmB, kt * kBK, nb, fb);
                     } else {
                         ptx::mbar_arrive_expect_tx(&full[s], Cf::kTx);
-                        tma_load_2d(st, &tmA, kt * kBK, ma, &full[s]);
+                        tma_load_2d(st, &tmA, ax, ay, &full[s]);
                         if (g.swiglu) {  // two 128-row boxes: gate rows, then up rows
                             tma_load_2d(st + Cf::kATile, &tmB, kt * kBK, nb, &full[s]);
                             tma_load_2d(st + Cf::kATile + 128 * kBK * 2, &tmB, kt * kBK, nb + (int) g.F, &full[s]);
@@ -827,6 +844,14 @@ extern "C" size_t acb_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
     return sp > 1 ? (size_t) sp * (size_t) M * (size_t) N * 4 : 0;
 }
 
+// acb_gemm_tc and acb_conv1d_tc: a_cols = the columns of A's tensor map (K, or the channel count
+// of an implicit convolution, whose conv_* fields are already set in g0)
+static acb_status gemm_tc_launch(GemmArgs g0, const void * A, int64_t lda, int64_t a_cols, const void * B,
+                                 int64_t ldb, int64_t M, int64_t N, int64_t K, void * C, int c_type, int64_t ldc,
+                                 const float * bias, const float * res, int64_t ldr, const float * gate,
+                                 int64_t gate_stride, int64_t rows_per_sample, int flags, void * workspace,
+                                 size_t workspace_bytes, int * err_flag, acb_stream_t stream);
+
 extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int64_t ldb, int64_t M, int64_t N,
                                   int64_t K, void * C, int c_type, int64_t ldc, const float * bias, const float * res,
                                   int64_t ldr, const float * gate, int64_t gate_stride, int64_t rows_per_sample,
@@ -835,6 +860,39 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
     if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || lda < K || ldb < K || ldc < N) {
         return ACB_ERR_INVALID_ARG;
     }
+    return gemm_tc_launch(GemmArgs{}, A, lda, K, B, ldb, M, N, K, C, c_type, ldc, bias, res, ldr, gate, gate_stride,
+                          rows_per_sample, flags, workspace, workspace_bytes, err_flag, stream);
+}
+
+extern "C" acb_status acb_conv1d_tc(const void * X, int64_t ldx, int64_t T, int C_in, const void * W, int64_t N,
+                                    int kernel, int dilation, int pad, void * Y, int y_type, int64_t ldy,
+                                    const float * bias, const float * res, int64_t ldr, int flags, void * workspace,
+                                    size_t workspace_bytes, int * err_flag, acb_stream_t stream) {
+    if (!X || !W || !Y || T <= 0 || C_in <= 0 || N <= 0 || kernel <= 0 || dilation <= 0 || pad < 0 ||
+        ldx < C_in || ldy < N) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (C_in % kBK != 0) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    // rows reached by the taps stay within int range for the TMA coordinates
+    if (T + (int64_t) (kernel - 1) * dilation > INT32_MAX / 2 || (int64_t) kernel * C_in > INT32_MAX / 2) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    GemmArgs g0 = {};
+    g0.conv_c   = C_in;
+    g0.conv_dil = dilation;
+    g0.conv_pad = pad;
+    const int64_t K = (int64_t) kernel * C_in;
+    return gemm_tc_launch(g0, X, ldx, C_in, W, K, T, N, K, Y, y_type, ldy, bias, res, ldr, nullptr, 0, 1, flags,
+                          workspace, workspace_bytes, err_flag, stream);
+}
+
+static acb_status gemm_tc_launch(GemmArgs g0, const void * A, int64_t lda, int64_t a_cols, const void * B,
+                                 int64_t ldb, int64_t M, int64_t N, int64_t K, void * C, int c_type, int64_t ldc,
+                                 const float * bias, const float * res, int64_t ldr, const float * gate,
+                                 int64_t gate_stride, int64_t rows_per_sample, int flags, void * workspace,
+                                 size_t workspace_bytes, int * err_flag, acb_stream_t stream) {
     if (K % kBK != 0 || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0 || reinterpret_cast<uintptr_t>(A) % 16 != 0 ||
         reinterpret_cast<uintptr_t>(B) % 16 != 0) {
         return ACB_ERR_UNSUPPORTED;
@@ -845,7 +903,7 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
     if (gate && (!res || rows_per_sample <= 0)) {
         return ACB_ERR_INVALID_ARG;
     }
-    GemmArgs g        = {};
+    GemmArgs g        = g0;
     g.M               = M;
     g.N               = N;
     g.K               = K;
@@ -877,7 +935,7 @@ extern "C" acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, i
     const int  clusters = g.splits == 1 && M > 128 ? pair_clusters(f16) : 0;
     const bool pair     = clusters > 0;
     CUtensorMap ta, tb;
-    if (!make_map(&ta, A, M, K, lda, 128, f16) || !make_map(&tb, B, N, K, ldb, pair ? 128 : kBN, f16)) {
+    if (!make_map(&ta, A, M, a_cols, lda, 128, f16) || !make_map(&tb, B, N, K, ldb, pair ? 128 : kBN, f16)) {
         return ACB_ERR_CUDA;
     }
     g.group_m              = group_m_for(pair ? (M + 255) / 256 : (M + 127) / 128);

@@ -1,0 +1,201 @@
+// k_vae.cu -- the AutoencoderOobleck decoder's non-GEMM ops (src/vae.h:270-364). Its convolutions
+// run on the tensor-core GEMM (acb_conv1d_tc, an implicit GEMM: TMA reads each tap's rows of the
+// f16 activation directly, with zero fill outside [0, T)); the operands come from here:
+//
+//   acb_vae_snake_f16     y[t][c] = f16(snake(x[t][c])): the snake activation x + sin(x*e^a)^2 *
+//                         e^-b (vae_snake, :270-280, five separately rounded f32 ops), rounded to
+//                         the f16 operand type ggml_conv_1d gives the activation (its im2col takes
+//                         the weights' type). Without e^a a plain cast (the first conv's input).
+//   acb_vae_col2im        y[t][oc] = bias[oc] + the conv-transpose columns that land on t
+//                         (ggml_col2im_1d of vae_conv_t1d, :300-323): the GEMM gives
+//                         col[t_in][k*OC + oc] = x[t_in] . w[:, oc, k]; output t gathers
+//                         k = (t + pad) - t_in*stride for every t_in, in ascending k.
+//   acb_vae_out_conv      the last conv (C -> 2 channels, k = 7, no bias) with its snake, as a
+//                         direct convolution: 2 outputs per sample are too few for a GEMM tile.
+//                         Output planar [2][T] (ggml's [T, 2] with T contiguous).
+#include "common.cuh"
+
+namespace acb {
+namespace {
+
+__device__ __forceinline__ float snake_f(float x, float ea, float ib) {
+    const float ax = __fmul_rn(x, ea);
+    const float s  = sinf(ax);
+    return __fadd_rn(x, __fmul_rn(__fmul_rn(s, s), ib));
+}
+
+// one thread per 8 consecutive channels of one row; C a multiple of 8
+__global__ void snake_f16_kernel(const float * __restrict__ x, int64_t xs, int64_t T, int C,
+                                 const float * __restrict__ ea, const float * __restrict__ ib,
+                                 __half * __restrict__ y, int64_t ldy) {
+    const int     groups = C / 8;
+    const int64_t idx    = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= T * groups) {
+        return;
+    }
+    const int64_t t  = idx / groups;
+    const int     c0 = (int) (idx - t * groups) * 8;
+    const float4  a  = *reinterpret_cast<const float4 *>(x + t * xs + c0);
+    const float4  b  = *reinterpret_cast<const float4 *>(x + t * xs + c0 + 4);
+    const float   v[8] = { a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w };
+    union {
+        uint4  u;
+        __half h[8];
+    } o;
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+        o.h[e] = __float2half_rn(ea ? snake_f(v[e], __ldg(ea + c0 + e), __ldg(ib + c0 + e)) : v[e]);
+    }
+    *reinterpret_cast<uint4 *>(y + t * ldy + c0) = o.u;
+}
+
+__global__ void col2im_kernel(const float * __restrict__ col, int64_t T_in, int OC, int Kc, int stride, int pad,
+                              const float * __restrict__ bias, float * __restrict__ y, int64_t T_out) {
+    const int64_t idx = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= T_out * OC) {
+        return;
+    }
+    const int64_t t  = idx / OC;
+    const int     oc = (int) (idx - t * OC);
+    const int64_t u  = t + pad;  // position before cropping
+    float         acc = 0.0f;
+    for (int k = (int) (u % stride); k < Kc; k += stride) {
+        const int64_t ti = (u - k) / stride;
+        if (ti >= 0 && ti < T_in) {
+            acc = __fadd_rn(acc, col[ti * ((int64_t) Kc * OC) + (int64_t) k * OC + oc]);
+        }
+    }
+    y[idx] = bias ? __fadd_rn(acc, bias[oc]) : acc;
+}
+
+// Final conv, C channels -> 2, k = 7, pad 3, with the snake. A CTA of 8 warps covers 128 samples:
+// the snake'd f16 inputs of samples [t0 - 3, t0 + 131) and the f16 weights are staged in shared
+// memory once; a warp computes one sample at a time with its lanes across channel quads
+// (consecutive 8-byte reads, no bank conflicts), f32 products and sums, reduced over the lanes.
+constexpr int kOutTile = 128, kOutThreads = 256;
+
+__global__ void __launch_bounds__(kOutThreads) out_conv_kernel(const float * __restrict__ x, int64_t T, int C,
+                                                               const float * __restrict__ ea,
+                                                               const float * __restrict__ ib,
+                                                               const __half * __restrict__ w,  // [2][7][C]
+                                                               float * __restrict__ y) {
+    extern __shared__ __align__(16) __half os_smem[];  // [kOutTile + 6][C] inputs, [14][C] weights
+    __half *      xs = os_smem;
+    __half *      wsm = os_smem + (kOutTile + 6) * C;
+    __shared__ float res[2][kOutTile];
+    const int64_t t0 = (int64_t) blockIdx.x * kOutTile;
+    const int     cq = C / 4;
+    for (int i = threadIdx.x; i < (kOutTile + 6) * cq; i += blockDim.x) {
+        const int     r  = i / cq, c = (i - r * cq) * 4;
+        const int64_t ts = t0 - 3 + r;
+        union {
+            uint2  u;
+            __half h[4];
+        } o;
+        if (ts >= 0 && ts < T) {
+            const float4 v = *reinterpret_cast<const float4 *>(x + ts * C + c);
+            o.h[0]         = __float2half_rn(snake_f(v.x, __ldg(ea + c), __ldg(ib + c)));
+            o.h[1]         = __float2half_rn(snake_f(v.y, __ldg(ea + c + 1), __ldg(ib + c + 1)));
+            o.h[2]         = __float2half_rn(snake_f(v.z, __ldg(ea + c + 2), __ldg(ib + c + 2)));
+            o.h[3]         = __float2half_rn(snake_f(v.w, __ldg(ea + c + 3), __ldg(ib + c + 3)));
+        } else {
+            o.u = make_uint2(0, 0);
+        }
+        *reinterpret_cast<uint2 *>(xs + r * C + c) = o.u;
+    }
+    for (int i = threadIdx.x; i < 14 * cq; i += blockDim.x) {
+        *reinterpret_cast<uint2 *>(wsm + i * 4) = *reinterpret_cast<const uint2 *>(w + i * 4);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int s = warp; s < kOutTile; s += kOutThreads / 32) {
+        float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 7; k++) {
+            for (int q = lane; q < cq; q += 32) {
+                union {
+                    uint2  u;
+                    __half h[4];
+                } xv, w0, w1;
+                xv.u = *reinterpret_cast<const uint2 *>(xs + (s + k) * C + 4 * q);
+                w0.u = *reinterpret_cast<const uint2 *>(wsm + k * C + 4 * q);
+                w1.u = *reinterpret_cast<const uint2 *>(wsm + (7 + k) * C + 4 * q);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float xf = __half2float(xv.h[e]);
+                    a0             = fmaf(xf, __half2float(w0.h[e]), a0);
+                    a1             = fmaf(xf, __half2float(w1.h[e]), a1);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+            a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+        }
+        if (lane == 0) {
+            res[0][s] = a0;
+            res[1][s] = a1;
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 2 * kOutTile; i += blockDim.x) {
+        const int     ch = i / kOutTile, s = i - ch * kOutTile;
+        const int64_t t  = t0 + s;
+        if (t < T) {
+            y[ch * T + t] = res[ch][s];
+        }
+    }
+}
+
+}  // namespace
+}  // namespace acb
+
+using namespace acb;
+
+extern "C" acb_status acb_vae_snake_f16(const float * x, int64_t x_stride, int64_t T, int C, const float * exp_alpha,
+                                        const float * inv_beta, void * y, int64_t ldy, acb_stream_t stream) {
+    if (!x || !y || T <= 0 || C <= 0 || x_stride < C || ldy < C || (exp_alpha && !inv_beta)) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    if (C % 8 || x_stride % 4 || ldy % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(y) & 15)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    const int64_t n = T * (C / 8);
+    snake_f16_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(
+        x, x_stride, T, C, exp_alpha, inv_beta, reinterpret_cast<__half *>(y), ldy);
+    return launch_status();
+}
+
+extern "C" acb_status acb_vae_col2im(const float * col, int64_t T_in, int OC, int kernel, int stride, int pad,
+                                     const float * bias, float * y, acb_stream_t stream) {
+    if (!col || !y || T_in <= 0 || OC <= 0 || kernel <= 0 || stride <= 0 || pad < 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int64_t T_out = (T_in - 1) * stride + kernel - 2 * pad;
+    if (T_out <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int64_t n = T_out * OC;
+    col2im_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(col, T_in, OC, kernel, stride,
+                                                                                   pad, bias, y, T_out);
+    return launch_status();
+}
+
+extern "C" acb_status acb_vae_out_conv(const float * x, int64_t T, int C, const float * exp_alpha,
+                                       const float * inv_beta, const void * w, float * y, acb_stream_t stream) {
+    if (!x || !w || !y || !exp_alpha || !inv_beta || T <= 0 || C <= 0) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const size_t smem = (size_t) (kOutTile + 6 + 14) * C * 2;
+    if (C % 4 || smem > 200 * 1024 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 7)) {
+        return ACB_ERR_UNSUPPORTED;
+    }
+    if (smem > 48 * 1024) {
+        cudaFuncSetAttribute(out_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+    }
+    out_conv_kernel<<<(unsigned) ((T + kOutTile - 1) / kOutTile), kOutThreads, smem, (cudaStream_t) stream>>>(
+        x, T, C, exp_alpha, inv_beta, reinterpret_cast<const __half *>(w), y);
+    return launch_status();
+}

@@ -314,3 +314,71 @@ def write_dit_gguf(path: str, cfg: dict, qtype: int = Q8_0, seed: int = 0, devic
     w.write_tensors_to_file()
     w.close()
     return total
+
+
+# ---- VAE decoder (src/vae.h) ---------------------------------------------------------------------
+
+ACESTEP_VAE = dict(latent=64, c0=2048, in_ch=[2048, 1024, 512, 256, 128], out_ch=[1024, 512, 256, 128, 128],
+                   strides=[10, 6, 4, 4, 2])
+VAE_TINY = dict(latent=64, c0=256, in_ch=[256, 128, 128, 64, 64], out_ch=[128, 128, 64, 64, 64],
+                strides=[10, 6, 4, 4, 2])
+
+
+def vae_tensors(vcfg: dict, seed: int = 0):
+    """Yields (name, numpy float32 array in PyTorch shape) of an AutoencoderOobleck decoder with the
+    reference's GGUF names (vae.h:200-240): weight-normalised convs (weight_g [OC,1,1], weight_v),
+    biases, snake alpha / beta [1, C, 1]. Stored BF16 by write_vae_gguf, as convert.py does.
+    Conditioned like a trained residual decoder, so that rounding differences stay small at the
+    output: residual branches end in a small gain (conv2 weight_g 0.1-0.3) and the snake's
+    periodic term is damped (beta around 1, e^-beta around 0.37). With unit gains everywhere a
+    1e-6 input perturbation moved the output by 2e-2 at this depth."""
+    rng = np.random.default_rng(seed)
+
+    def wn(pfx, shape, dim0, g=(0.6, 1.2)):
+        yield f"{pfx}.weight_g", rng.uniform(g[0], g[1], (dim0, 1, 1)).astype(np.float32)
+        yield f"{pfx}.weight_v", rng.standard_normal(shape).astype(np.float32)
+
+    def snake(pfx, C):
+        yield f"{pfx}.alpha", (0.2 * rng.standard_normal((1, C, 1))).astype(np.float32)
+        yield f"{pfx}.beta", (1.0 + 0.2 * rng.standard_normal((1, C, 1))).astype(np.float32)
+
+    c0, L = vcfg["c0"], vcfg["latent"]
+    yield from wn("decoder.conv1", (c0, L, 7), c0)
+    yield "decoder.conv1.bias", (0.05 * rng.standard_normal(c0)).astype(np.float32)
+    for i, (ic, oc, s) in enumerate(zip(vcfg["in_ch"], vcfg["out_ch"], vcfg["strides"])):
+        p = f"decoder.block.{i}"
+        yield from snake(f"{p}.snake1", ic)
+        yield from wn(f"{p}.conv_t1", (ic, oc, 2 * s), ic)
+        yield f"{p}.conv_t1.bias", (0.05 * rng.standard_normal(oc)).astype(np.float32)
+        for r in range(1, 4):
+            rp = f"{p}.res_unit{r}"
+            yield from snake(f"{rp}.snake1", oc)
+            yield from wn(f"{rp}.conv1", (oc, oc, 7), oc)
+            yield f"{rp}.conv1.bias", (0.05 * rng.standard_normal(oc)).astype(np.float32)
+            yield from snake(f"{rp}.snake2", oc)
+            yield from wn(f"{rp}.conv2", (oc, oc, 1), oc, g=(0.1, 0.3))
+            yield f"{rp}.conv2.bias", (0.05 * rng.standard_normal(oc)).astype(np.float32)
+    cl = vcfg["out_ch"][-1]
+    yield from snake("decoder.snake1", cl)
+    yield from wn("decoder.conv2", (2, cl, 7), 2)
+
+
+def write_vae_gguf(path: str, vcfg: dict, seed: int = 0, keep: dict | None = None) -> int:
+    """An acestep-vae GGUF with every tensor BF16 (rounded to nearest even). keep receives
+    name -> bf16 bits (numpy uint16, PyTorch shape)."""
+    import gguf
+    w = gguf.GGUFWriter(path, "acestep-vae")
+    total = 0
+    for name, a in vae_tensors(vcfg, seed):
+        u = a.view(np.uint32)  # finite values: u + 0x8000 stays below 2^32
+        bits = ((u + (np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1)))) >> 16).astype(np.uint16)
+        w.add_tensor(name, bits.view(np.uint8).reshape(*a.shape[:-1], a.shape[-1] * 2),
+                     raw_dtype=gguf.GGMLQuantizationType.BF16)
+        total += bits.nbytes
+        if keep is not None:
+            keep[name] = bits
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return total

@@ -295,6 +295,18 @@ ACB_API acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int6
                                int flags, void * workspace, size_t workspace_bytes, int * err_flag,
                                acb_stream_t stream);
 
+/* 1-D convolution as an implicit GEMM on the same tensor-core kernel (ggml_conv_1d = im2col +
+ * mul_mat, src/vae.h:283-297, without the im2col buffer):
+ *   Y[t][n] = epi( sum_{k, c} X[t + k*dilation - pad][c] * W[n][k*C_in + c] ),
+ * X [T][ldx] bf16 / f16 (ACB_FLAG_F16) rows of C_in channels, rows outside [0, T) read as 0 (the
+ * TMA bounds fill), W [N][kernel*C_in] in the same type, stride 1, T_out = T when
+ * 2*pad = (kernel-1)*dilation. Epilogue, workspace, flags and Y types as acb_gemm_tc. C_in a
+ * multiple of 64 (one 64-channel slice of one tap per k-tile). */
+ACB_API acb_status acb_conv1d_tc(const void * X, int64_t ldx, int64_t T, int C_in, const void * W, int64_t N,
+                                 int kernel, int dilation, int pad, void * Y, int y_type, int64_t ldy,
+                                 const float * bias, const float * res, int64_t ldr, int flags, void * workspace,
+                                 size_t workspace_bytes, int * err_flag, acb_stream_t stream);
+
 /* Attention over whole sequences (flash tiling on tensor cores, fp32 softmax and
  * accumulation), head_dim 128, GQA head h -> kv head h / (Nh/Nkv):
  *   O[b,i,h] = softmax_j(Q[b,i,h].K[b,j,h'] * scale + mask) V[b,j,h']
@@ -421,6 +433,24 @@ ACB_API acb_status acb_rows_repeat_add(const float * a, int64_t lda, const float
  * Alignment as acb_rows_repeat_add. */
 ACB_API acb_status acb_rows_prepend(const float * head, const float * src, int64_t lds, int G, int P, int H,
                                     float * out, int64_t ldo, acb_stream_t stream);
+
+/* ---- VAE decoder ops (src/vae.h) -------------------------------------------------------------- */
+
+/* y [T][ldy] f16 = f16(snake(x)) with the snake x + sin(x*e^a)^2 * e^-b (vae_snake, src/vae.h:
+ * 270-280: exp_alpha = e^a, inv_beta = e^-b per channel, five separately rounded f32 ops; NULL:
+ * no snake, a plain cast). f16 is the operand type ggml_conv_1d gives the activation (its im2col
+ * takes the f16 weights' type); acb_conv1d_tc reads y in place of the im2col. C, x_stride, ldy
+ * multiples of 8, x and y 16-byte aligned. */
+ACB_API acb_status acb_vae_snake_f16(const float * x, int64_t x_stride, int64_t T, int C, const float * exp_alpha,
+                                     const float * inv_beta, void * y, int64_t ldy, acb_stream_t stream);
+/* ConvTranspose1d overlap-add: col [T_in][kernel*OC] (column k*OC + oc of input step t_in) ->
+ * y [T_out][OC], T_out = (T_in - 1)*stride + kernel - 2*pad, plus bias (NULL: none). */
+ACB_API acb_status acb_vae_col2im(const float * col, int64_t T_in, int OC, int kernel, int stride, int pad,
+                                  const float * bias, float * y, acb_stream_t stream);
+/* The output conv: snake, then C -> 2 channels, kernel 7, pad 3, no bias; w f16 [2][7][C];
+ * y planar [2][T]. */
+ACB_API acb_status acb_vae_out_conv(const float * x, int64_t T, int C, const float * exp_alpha,
+                                    const float * inv_beta, const void * w, float * y, acb_stream_t stream);
 
 /* ---- LM token sampling ------------------------------------------------------------------------ */
 

@@ -14,6 +14,10 @@
 extern "C" {
 #endif
 
+/* Cancellation callback, polled between steps of a long call (denoise steps, dit-sampler.h:409-413;
+ * VAE tiles, vae.h:536): nonzero stops the call with ACB_ERR_CANCELLED. */
+typedef int (*acb_cancel_fn)(void * data);
+
 /* ---- GGUF (replaces gf_load / gf_close / gf_get_*, src/gguf-weights.h:48-155,357-390) ---- */
 
 typedef struct acb_gguf acb_gguf;
@@ -132,6 +136,32 @@ ACB_API acb_status acb_cond_forward_device(acb_cond * m, const float * d_text_hi
  * guidance (CondGGML.null_cond_emb). */
 ACB_API acb_status acb_cond_null_embedding(acb_cond * m, float * out);
 ACB_API void       acb_cond_free(acb_cond * m); /* cond_ggml_free :383 */
+
+/* ---- VAE decoder (replaces src/vae.h) --------------------------------------------------------- */
+
+typedef struct acb_vae acb_vae;
+
+/* vae_ggml_load (vae.h:128-250): decoder.* of an acestep-vae GGUF (BF16 weight_g / weight_v,
+ * biases, snake alpha / beta). Weight normalisation is fused at load as the reference does it and
+ * the weights kept in f16; channels and strides come from the tensor shapes (channel counts must
+ * be multiples of 64). */
+ACB_API acb_status acb_vae_load(const char * gguf_path, int device, acb_vae ** out);
+ACB_API int        acb_vae_upsample(const acb_vae * m); /* audio samples per latent frame (1920) */
+/* vae_ggml_decode (vae.h:466-488): latent [T_latent][64] (host, time-major as the DiT writes it)
+ * -> audio_out [2][T_audio] (host: channel 0 then channel 1), T_audio = T_latent * upsample <=
+ * max_T_audio. Convolutions run as tcgen05 GEMMs on f16 operands (ggml's conv_1d casts the
+ * activation to the f16 weights), snake activations in f32. */
+ACB_API acb_status acb_vae_decode(acb_vae * m, const float * latent, int T_latent, float * audio_out,
+                                  int max_T_audio, int * out_T_audio);
+/* vae_ggml_decode_tiled (vae.h:495-585): the same windows (chunk_size frames plus overlap of
+ * context each side, reference defaults 256 / 64), trims and layout; cancel is polled per tile. */
+ACB_API acb_status acb_vae_decode_tiled(acb_vae * m, const float * latent, int T_latent, float * audio_out,
+                                        int max_T_audio, int chunk_size, int overlap, acb_cancel_fn cancel,
+                                        void * cancel_data, int * out_T_audio);
+/* Device buffers: d_latent [T_latent][64] -> d_audio [2][T_latent * upsample]; synchronises. */
+ACB_API acb_status acb_vae_decode_device(acb_vae * m, const float * d_latent, int T_latent, float * d_audio,
+                                         acb_stream_t stream);
+ACB_API void       acb_vae_free(acb_vae * m); /* vae_ggml_free :567 */
 
 /* ---- FSQ detokenizer and tokenizer (replace src/fsq-detok.h, src/fsq-tok.h) ------------------ */
 
@@ -296,8 +326,6 @@ ACB_API acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, con
                                            const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                            const float * schedule, float * output, float guidance_scale, int solver,
                                            float * gpu_ms);
-/* Cancellation callback polled before every denoise step (dit-sampler.h:409-413): nonzero stops. */
-typedef int (*acb_cancel_fn)(void * data);
 /* Noise source of the SDE solver: n N(0,1) samples of the stream seeded with `seed` into out. The
  * reference's is philox_randn(seed, out, n, true) (src/philox.h: Philox4x32-10, rounded to bf16);
  * a caller binding ace-synth passes that function, so trajectories match the reference's. */

@@ -1025,3 +1025,127 @@ def lora_merge(entry, A, B, scaling):
     else:
         out = quantize(merged, qt)
     return qt, out, merged
+
+
+# ---- VAE decoder (src/vae.h) ----------------------------------------------------------------------
+
+class OracleVAE:
+    """vae_ggml_load + vae_ggml_build_graph (src/vae.h:128-388) in numpy over the GGUF's bf16 bits
+    {name: uint16 array in PyTorch shape}: weight norm fused in f32 with a sequential sum of squares
+    (vae_fuse_wn, :63-91) and rounded to f16; snake in f32 (five separately rounded ops); every conv
+    as an im2col of f16-cast activations times the f16 weights, exact products summed in float64
+    and rounded to f32 (ggml_conv_1d's operand types; the sum order of ggml is not reproduced);
+    ConvTranspose as that GEMM plus the overlap-add in ascending kernel tap, then the bias."""
+
+    def __init__(self, bits: dict):
+        f = lambda n: bf16_bits_to_f32(bits[n]).reshape(bits[n].shape)
+        self.f = f
+        self.c1 = self._conv(f, "decoder.conv1", bias=True)
+        self.blocks = []
+        i = 0
+        while f"decoder.block.{i}.conv_t1.weight_v" in bits:
+            p = f"decoder.block.{i}"
+            g, v = f(f"{p}.conv_t1.weight_g"), f(f"{p}.conv_t1.weight_v")  # v [IC, OC, K]
+            w = self._wn(g.reshape(-1), v).astype(np.float16)
+            ru = []
+            for r in range(1, 4):
+                rp = f"{p}.res_unit{r}"
+                ru.append(dict(s1=self._snake(f, f"{rp}.snake1"), c1=self._conv(f, f"{rp}.conv1", True),
+                               s2=self._snake(f, f"{rp}.snake2"), c2=self._conv(f, f"{rp}.conv2", True),
+                               dil=(1, 3, 9)[r - 1]))
+            self.blocks.append(dict(sn=self._snake(f, f"{p}.snake1"), ct=w, ctb=f(f"{p}.conv_t1.bias").reshape(-1),
+                                    stride=v.shape[2] // 2, ru=ru))
+            i += 1
+        self.sn = self._snake(f, "decoder.snake1")
+        self.c2 = self._conv(f, "decoder.conv2", bias=False)
+        self.up = int(np.prod([b["stride"] for b in self.blocks]))
+
+    @staticmethod
+    def _wn(g, v):
+        d0 = v.shape[0]
+        vv = v.reshape(d0, -1).astype(np.float32)
+        sq = (vv * vv).astype(np.float32)
+        nsq = np.add.accumulate(sq, axis=1, dtype=np.float32)[:, -1]  # sequential f32 sum
+        s = (g.astype(np.float32) / (np.sqrt(nsq).astype(np.float32) + np.float32(1e-12))).astype(np.float32)
+        return (vv * s[:, None]).astype(np.float32).reshape(v.shape)
+
+    def _conv(self, f, pfx, bias):
+        v = f(f"{pfx}.weight_v")  # [OC, IC, K]
+        w = self._wn(f(f"{pfx}.weight_g").reshape(-1), v).astype(np.float16)
+        return dict(w=w, b=f(f"{pfx}.bias").reshape(-1) if bias else None)
+
+    @staticmethod
+    def _snake(f, pfx):
+        a = f(f"{pfx}.alpha").reshape(-1)
+        b = f(f"{pfx}.beta").reshape(-1)
+        return np.exp(a).astype(np.float32), (np.float32(1.0) / np.exp(b).astype(np.float32)).astype(np.float32)
+
+    @staticmethod
+    def snake(x, sn):
+        ea, ib = sn
+        ax = (x * ea).astype(np.float32)
+        s = np.sin(ax).astype(np.float32)
+        return (x + ((s * s).astype(np.float32) * ib).astype(np.float32)).astype(np.float32)
+
+    @staticmethod
+    def conv(x, c, dil=1, pad=None, res=None):
+        """x [T][IC] f32 -> [T][OC]: f16 im2col, exact f16 products summed in float64."""
+        w = c["w"]  # [OC, IC, K] f16
+        OC, IC, K = w.shape
+        pad = (K // 2) * dil if pad is None else pad
+        T = x.shape[0]
+        xh = x.astype(np.float16).astype(np.float64)
+        xp = np.zeros((T + 2 * pad, IC))
+        xp[pad:pad + T] = xh
+        y = np.zeros((T, OC))
+        wf = w.astype(np.float64)
+        for k in range(K):
+            y += xp[k * dil:k * dil + T] @ wf[:, :, k].T
+        y = y.astype(np.float32)
+        if c["b"] is not None:
+            y = (y + c["b"]).astype(np.float32)
+        if res is not None:
+            y = (res + y).astype(np.float32)
+        return y
+
+    def decode(self, latent):
+        """latent [T][64] -> audio [2][T * up]."""
+        x = self.conv(np.asarray(latent, np.float32), self.c1)
+        for b in self.blocks:
+            h = self.snake(x, b["sn"]).astype(np.float16).astype(np.float64)
+            w = b["ct"].astype(np.float64)  # [IC, OC, K]
+            IC, OC, K = w.shape
+            s = b["stride"]
+            col = np.tensordot(h, w, axes=([1], [0])).astype(np.float32)  # [T][OC][K]
+            T = x.shape[0]
+            pad = (K - s) // 2
+            full = np.zeros(((T - 1) * s + K, OC), np.float32)
+            for k in range(K):  # overlap-add in ascending tap: input t lands on t*s + k
+                full[k:k + (T - 1) * s + 1:s] += col[:, :, k]
+            y = full[pad:pad + (T - 1) * s + K - 2 * pad]
+            x = (y + b["ctb"]).astype(np.float32)
+            for r in b["ru"]:
+                h1 = self.conv(self.snake(x, r["s1"]), r["c1"], dil=r["dil"])
+                x = self.conv(self.snake(h1, r["s2"]), r["c2"], res=x)
+        y = self.conv(self.snake(x, self.sn), self.c2)  # [T][2]
+        return np.ascontiguousarray(y.T)
+
+    def decode_tiled(self, latent, chunk_size=256, overlap=64):
+        """vae_ggml_decode_tiled (src/vae.h:495-585) over decode()."""
+        T = latent.shape[0]
+        while chunk_size - 2 * overlap <= 0 and overlap > 0:
+            overlap //= 2
+        if T <= chunk_size:
+            return self.decode(latent)
+        stride = chunk_size - 2 * overlap
+        outs, upf = [], None
+        for i in range((T + stride - 1) // stride):
+            c0, c1 = i * stride, min(i * stride + stride, T)
+            w0, w1 = max(c0 - overlap, 0), min(c1 + overlap, T)
+            a = self.decode(latent[w0:w1])
+            if upf is None:
+                upf = np.float32(a.shape[1]) / np.float32(w1 - w0)
+            t0 = int(np.round(np.float32(c0 - w0) * upf))
+            t1 = int(np.round(np.float32(w1 - c1) * upf))
+            outs.append(a[:, t0:(a.shape[1] - t1 if t1 > 0 else a.shape[1])])
+        return np.concatenate(outs, axis=1)
