@@ -116,6 +116,15 @@ __device__ __forceinline__ float silu_times(float g, float u) {
     return __fmul_rn(s, u);
 }
 
+// The VAE's snake activation x + sin(x * e^a)^2 * e^-b (src/vae.h:270-280, ggml_mul, ggml_sin,
+// ggml_sqr, ggml_mul, ggml_add: each node rounded once); ea = e^a, ib = e^-b per channel. One
+// definition for the standalone kernel and the GEMM epilogue that fuses it.
+__device__ __forceinline__ float snake_f(float x, float ea, float ib) {
+    const float ax = __fmul_rn(x, ea);
+    const float s  = sinf(ax);
+    return __fadd_rn(x, __fmul_rn(__fmul_rn(s, s), ib));
+}
+
 __device__ __forceinline__ float rms_scale(double sumsq, int n, float eps) {
     float mean = (float) (sumsq / (double) n);
     return 1.0f / sqrtf(__fadd_rn(mean, eps));

@@ -145,6 +145,31 @@ __device__ __forceinline__ float4 load_cols(const float * src, int ncol) {
                        ncol > 3 ? src[3] : 0.0f);
 }
 
+// C[off .. off+ncol) = v in C's type
+__device__ __forceinline__ void store_c(const GemmArgs & g, int64_t off, float4 v, int ncol) {
+    if (g.c_type == ACB_TYPE_F32) {
+        store_cols<ACB_TYPE_F32>(g.C, off, v, ncol);
+    } else if (g.c_type == ACB_TYPE_BF16) {
+        store_cols<ACB_TYPE_BF16>(g.C, off, v, ncol);
+    } else {
+        store_cols<ACB_TYPE_F16>(g.C, off, v, ncol);
+    }
+}
+
+// The residual of one 32 x 32 chunk as this lane reads it in the plain epilogue (rows it*4 + sub,
+// columns cc .. cc+3), loaded ahead of the chunk's stores: res may alias C, so loads issued inside
+// the store loop would each wait for the previous store (one memory round trip per 4 rows).
+__device__ __forceinline__ void load_res_chunk(const GemmArgs & g, int64_t m_base, int64_t nc, int sub, int cc,
+                                               float4 (&rv)[8]) {
+    const int64_t n    = nc + cc;
+    const int     ncol = (nc < g.N && n < g.N) ? (g.N - n < 4 ? (int) (g.N - n) : 4) : 0;
+#pragma unroll
+    for (int it = 0; it < 8; it++) {
+        const int64_t m = m_base + it * 4 + sub;
+        rv[it]          = (m < g.M && ncol > 0) ? load_cols(g.res + m * g.ldr + n, ncol) : make_float4(0, 0, 0, 0);
+    }
+}
+
 // SwiGLU epilogue of one warp: its 32 rows (m_base + lane) of the tile, features f0 .. f0+127.
 // Per 32-feature group: silu(gate) * up (ggml_swiglu, the unfused acb_act_quant_swiglu
 // arithmetic), then one Q8_0 block per row (d = amax / 127 stored as f16, q = round(y / d)) or a
@@ -586,8 +611,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int sub   = lane >> 3;       // row offset within a group of 4 rows
         const int cc    = (lane & 7) * 4;  // column offset within the chunk
         int       tile  = 0;
+        // plain residual epilogue: each chunk's residual is in registers before its stores, the
+        // first chunk's loaded while the tile's MMAs still run
+        const bool pre = !g.swiglu && !g.qkv && g.splits == 1 && g.epi == (g.epi & (EPI_BIAS | EPI_RES)) &&
+                         (g.epi & EPI_RES);
+        float4     rv[8], rvn[8];
         for (int64_t w = unit; w < n_work; w += n_units, tile++) {
             const int acc = tile & 1;
+            const int64_t t      = w % tiles;
+            int64_t mt, nt;
+            tile_mn(t, m_tiles, n_tiles, g.group_m, mt, nt);
+            const int64_t m_base = mt * Cf::kTileM + (int64_t) rank * 128 + q * 32;
+            if (pre) {
+                load_res_chunk(g, m_base, nt * kBN, sub, cc, rv);
+            }
             if (!ptx::mbar_wait(&tmem_full[acc], (tile >> 1) & 1)) {
                 if (lane == 0) {
                     flag_timeout(g.err);
@@ -596,10 +633,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int64_t t      = w % tiles;
-            int64_t mt, nt;
-            tile_mn(t, m_tiles, n_tiles, g.group_m, mt, nt);
-            const int64_t m_base = mt * Cf::kTileM + (int64_t) rank * 128 + q * 32;
             if (g.swiglu) {
                 swiglu_epilogue(g, tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN), m_base,
                                 nt * 128, lane, stg);
@@ -612,10 +645,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float *       pws    = part ? g.ws + (w / tiles) * g.M * g.N : nullptr;
 #pragma unroll 1
             for (int c = 0; c < kBN / 32; c++) {
+                if (pre && c + 1 < kBN / 32) {
+                    load_res_chunk(g, m_base, n0 + (c + 1) * 32, sub, cc, rvn);
+                }
                 uint32_t r[32];
                 tmem_ld32(tmem_base + ((uint32_t) (q * 32) << 16) + (uint32_t) (acc * kBN + c * 32), r);
                 const int64_t nc = n0 + c * 32;
                 if (nc >= g.N || m_base >= g.M) {
+                    if (pre) {
+#pragma unroll
+                        for (int it = 0; it < 8; it++) {
+                            rv[it] = rvn[it];
+                        }
+                    }
                     continue;  // warp-uniform: the whole chunk is outside C
                 }
 #pragma unroll
@@ -627,6 +669,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 __syncwarp();
                 const int64_t n    = nc + cc;
                 const int     ncol = n < g.N ? (g.N - n < 4 ? (int) (g.N - n) : 4) : 0;
+                if (pre) {
+                    // bias + prefetched residual (rv[it] is row it*4 + sub of this chunk)
+#pragma unroll
+                    for (int it = 0; it < 8; it++) {
+                        const int64_t m = m_base + it * 4 + sub;
+                        if (m < g.M && ncol > 0) {
+                            float4 v = *reinterpret_cast<const float4 *>(stg + (it * 4 + sub) * kStgPitch + cc);
+                            if (g.bias) {
+                                const float4 bv = load_cols(g.bias + n, ncol);
+                                v.x             = __fadd_rn(v.x, bv.x);
+                                v.y             = __fadd_rn(v.y, bv.y);
+                                v.z             = __fadd_rn(v.z, bv.z);
+                                v.w             = __fadd_rn(v.w, bv.w);
+                            }
+                            v.x = __fadd_rn(rv[it].x, v.x);
+                            v.y = __fadd_rn(rv[it].y, v.y);
+                            v.z = __fadd_rn(rv[it].z, v.z);
+                            v.w = __fadd_rn(rv[it].w, v.w);
+                            store_c(g, m * g.ldc + n, v, ncol);
+                        }
+                        rv[it] = rvn[it];
+                    }
+                    __syncwarp();
+                    continue;
+                }
 #pragma unroll 2
                 for (int it = 0; it < 8; it++) {
                     const int     rr = it * 4 + sub;
@@ -647,7 +714,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         v.w             = __fadd_rn(v.w, bv.w);
                     }
                     if (g.epi & (EPI_RES | EPI_GATED_RES)) {
-                        const float4 rv = load_cols(g.res + m * g.ldr + n, ncol);
+                        const float4 rs = load_cols(g.res + m * g.ldr + n, ncol);
                         if (g.epi & EPI_GATED_RES) {
                             const float4 gv = load_cols(g.gate + (m / g.rows_per_sample) * g.gate_stride + n, ncol);
                             v.x             = __fmul_rn(v.x, gv.x);
@@ -655,18 +722,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             v.z             = __fmul_rn(v.z, gv.z);
                             v.w             = __fmul_rn(v.w, gv.w);
                         }
-                        v.x = __fadd_rn(rv.x, v.x);
-                        v.y = __fadd_rn(rv.y, v.y);
-                        v.z = __fadd_rn(rv.z, v.z);
-                        v.w = __fadd_rn(rv.w, v.w);
+                        v.x = __fadd_rn(rs.x, v.x);
+                        v.y = __fadd_rn(rs.y, v.y);
+                        v.z = __fadd_rn(rs.z, v.z);
+                        v.w = __fadd_rn(rs.w, v.w);
                     }
-                    if (g.c_type == ACB_TYPE_F32) {
-                        store_cols<ACB_TYPE_F32>(g.C, m * g.ldc + n, v, ncol);
-                    } else if (g.c_type == ACB_TYPE_BF16) {
-                        store_cols<ACB_TYPE_BF16>(g.C, m * g.ldc + n, v, ncol);
-                    } else {
-                        store_cols<ACB_TYPE_F16>(g.C, m * g.ldc + n, v, ncol);
-                    }
+                    store_c(g, m * g.ldc + n, v, ncol);
                 }
                 __syncwarp();
             }

@@ -1,15 +1,12 @@
 // k_vae.cu -- the AutoencoderOobleck decoder's non-GEMM ops (src/vae.h:270-364). Its convolutions
 // run on the tensor-core GEMM (acb_conv1d_tc, an implicit GEMM: TMA reads each tap's rows of the
-// f16 activation directly, with zero fill outside [0, T)); the operands come from here:
+// f16 activation directly, with zero fill outside [0, T)), whose epilogue also applies the next
+// snake; what remains here:
 //
 //   acb_vae_snake_f16     y[t][c] = f16(snake(x[t][c])): the snake activation x + sin(x*e^a)^2 *
 //                         e^-b (vae_snake, :270-280, five separately rounded f32 ops), rounded to
 //                         the f16 operand type ggml_conv_1d gives the activation (its im2col takes
 //                         the weights' type). Without e^a a plain cast (the first conv's input).
-//   acb_vae_col2im        y[t][oc] = bias[oc] + the conv-transpose columns that land on t
-//                         (ggml_col2im_1d of vae_conv_t1d, :300-323): the GEMM gives
-//                         col[t_in][k*OC + oc] = x[t_in] . w[:, oc, k]; output t gathers
-//                         k = (t + pad) - t_in*stride for every t_in, in ascending k.
 //   acb_vae_out_conv      the last conv (C -> 2 channels, k = 7, no bias) with its snake, as a
 //                         direct convolution: 2 outputs per sample are too few for a GEMM tile.
 //                         Output planar [2][T] (ggml's [T, 2] with T contiguous).
@@ -17,12 +14,6 @@
 
 namespace acb {
 namespace {
-
-__device__ __forceinline__ float snake_f(float x, float ea, float ib) {
-    const float ax = __fmul_rn(x, ea);
-    const float s  = sinf(ax);
-    return __fadd_rn(x, __fmul_rn(__fmul_rn(s, s), ib));
-}
 
 // one thread per 8 consecutive channels of one row; C a multiple of 8
 __global__ void snake_f16_kernel(const float * __restrict__ x, int64_t xs, int64_t T, int C,
@@ -47,25 +38,6 @@ __global__ void snake_f16_kernel(const float * __restrict__ x, int64_t xs, int64
         o.h[e] = __float2half_rn(ea ? snake_f(v[e], __ldg(ea + c0 + e), __ldg(ib + c0 + e)) : v[e]);
     }
     *reinterpret_cast<uint4 *>(y + t * ldy + c0) = o.u;
-}
-
-__global__ void col2im_kernel(const float * __restrict__ col, int64_t T_in, int OC, int Kc, int stride, int pad,
-                              const float * __restrict__ bias, float * __restrict__ y, int64_t T_out) {
-    const int64_t idx = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= T_out * OC) {
-        return;
-    }
-    const int64_t t  = idx / OC;
-    const int     oc = (int) (idx - t * OC);
-    const int64_t u  = t + pad;  // position before cropping
-    float         acc = 0.0f;
-    for (int k = (int) (u % stride); k < Kc; k += stride) {
-        const int64_t ti = (u - k) / stride;
-        if (ti >= 0 && ti < T_in) {
-            acc = __fadd_rn(acc, col[ti * ((int64_t) Kc * OC) + (int64_t) k * OC + oc]);
-        }
-    }
-    y[idx] = bias ? __fadd_rn(acc, bias[oc]) : acc;
 }
 
 // Final conv, C channels -> 2, k = 7, pad 3, with the snake. A CTA of 8 warps covers 128 samples:
@@ -165,21 +137,6 @@ extern "C" acb_status acb_vae_snake_f16(const float * x, int64_t x_stride, int64
     const int64_t n = T * (C / 8);
     snake_f16_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(
         x, x_stride, T, C, exp_alpha, inv_beta, reinterpret_cast<__half *>(y), ldy);
-    return launch_status();
-}
-
-extern "C" acb_status acb_vae_col2im(const float * col, int64_t T_in, int OC, int kernel, int stride, int pad,
-                                     const float * bias, float * y, acb_stream_t stream) {
-    if (!col || !y || T_in <= 0 || OC <= 0 || kernel <= 0 || stride <= 0 || pad < 0) {
-        return ACB_ERR_INVALID_ARG;
-    }
-    const int64_t T_out = (T_in - 1) * stride + kernel - 2 * pad;
-    if (T_out <= 0) {
-        return ACB_ERR_INVALID_ARG;
-    }
-    const int64_t n = T_out * OC;
-    col2im_kernel<<<(unsigned) ((n + 255) / 256), 256, 0, (cudaStream_t) stream>>>(col, T_in, OC, kernel, stride,
-                                                                                   pad, bias, y, T_out);
     return launch_status();
 }
 

@@ -1,21 +1,29 @@
 // vae.cpp -- the AutoencoderOobleck audio decoder (src/vae.h) on libacb kernels: latents
 // [T][64] -> stereo audio [2][T * 1920].
 //
-//   conv1 (64 -> C0, k 7)                                   f16 cast, implicit-GEMM conv + bias
-//   5 blocks: snake -> ConvTranspose (stride s, k 2s)       snake (f16), GEMM, col2im + bias
-//             3 res units (dilation 1, 3, 9):
-//               snake -> conv k7 -> snake -> conv k1 -> + x snake (f16), implicit-GEMM conv + bias,
-//                                                         snake (f16), GEMM + bias + residual
-//                                                         (in place)
-//   snake -> conv2 (C -> 2, k 7, no bias)                   direct kernel, planar output
+//   conv1 (64 -> C0, k 7)                         f16 cast, implicit-GEMM conv + bias -> x (f32)
+//   5 blocks: snake -> ConvTranspose (s, k 2s)    snake (f16), 3-tap implicit-GEMM conv (below)
+//             3 res units (dilation 1, 3, 9):       + bias -> x
+//               snake -> conv k7 -> snake ->      snake (f16), k7 conv + bias -> h (f32), snake
+//               conv k1 -> + x                    (f16), k1 conv: x += v + bias (in place)
+//   snake -> conv2 (C -> 2, k 7, no bias)         direct kernel, planar output
 // Every convolution with more than two output channels is one tcgen05 GEMM (f16 operands, f32
-// accumulation): the k = 7 convs read their taps straight from the f16 activation
-// (acb_conv1d_tc, no im2col buffer); ggml's conv_1d casts the activation to the f16 weight type,
-// so the operands are those of the reference. Weight normalisation is fused at load exactly as
-// vae_fuse_wn / vae_fuse_wn_ct do (f32, sequential sum of squares), the weights rounded to f16 as
-// the reference stores them. Channel counts and strides come from the tensor shapes (the shipped
-// model: 2048 -> 1024 -> 512 -> 256 -> 128 -> 128, strides 10, 6, 4, 4, 2). Tiled decoding
-// (vae_ggml_decode_tiled) keeps the reference's windows and trims.
+// accumulation) reading its taps straight from the f16 activation (acb_conv1d_tc, no im2col):
+// ggml's conv_1d casts the activation to the f16 weight type, so the operands are those of the
+// reference. The snakes run as their own full-occupancy pass (acb_vae_snake_f16): folded into the
+// GEMM epilogue the sine made the four epilogue warps the bottleneck (36.8 instead of 20.4 ms for
+// 30 s of audio).
+// ConvTranspose1d with kernel 2s, stride s, padding s/2 (s even): output row s*q + r takes input
+// rows q-1 and q (r < s/2) or q and q+1 (r >= s/2), so it is a 3-tap convolution over the input
+// with s*OC output columns, phase-major ([T_in][s*OC] is the upsampled [T_in*s][OC]): the weights
+// are laid out W3[r*OC + oc][(j+1)*IC + ic] = w[ic][oc][k] for the tap k that phase r takes from
+// input row q + j (zero where a phase takes nothing from that row). The two contributions of
+// ggml_col2im_1d are summed inside the GEMM's f32 accumulation instead of after it.
+// Weight normalisation is fused at load exactly as vae_fuse_wn / vae_fuse_wn_ct do (f32,
+// sequential sum of squares), the weights rounded to f16 as the reference stores them. Channel
+// counts and strides come from the tensor shapes (the shipped model: 2048 -> 1024 -> 512 -> 256 ->
+// 128 -> 128, strides 10, 6, 4, 4, 2). Tiled decoding (vae_ggml_decode_tiled) keeps the
+// reference's windows and trims.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -50,9 +58,9 @@ struct ResUnit {
 
 struct Block {
     int     in_ch = 0, out_ch = 0, stride = 0, kernel = 0;
-    Snake   sn;
-    Conv    ct;  // B [kernel * out_ch][in_ch]: row k*OC + oc holds w[:, oc, k]
-    DevBuf  ctb;
+    Snake   sn;       // the snake in front of the transposed conv
+    Conv    ct;       // 3-tap form: B [stride * out_ch][3 * in_ch]
+    DevBuf  ctb;      // bias tiled over the stride phases [stride * out_ch]
     ResUnit ru[3];
 };
 
@@ -189,8 +197,7 @@ struct acb_vae {
     Snake        sn;           // final snake
     int          c_last = 0;   // channels into conv2
     DevBuf       c2w;          // [2][7][c_last] f16
-    DevBuf       x, h, A, col, ws, err, lat, out;
-    size_t       ws_bytes = 0;
+    DevBuf       x, h, a16, ws, err, lat, out;
 
     ~acb_vae() {
         cudaSetDevice(device);
@@ -207,16 +214,11 @@ struct acb_vae {
         return b.alloc(bytes, &b == &ws) == ACB_OK ? ACB_OK : ACB_ERR_OOM;
     }
 
-    // y [T][c.N] (rows ldy apart) = conv(A) (+ bias) (+ res) with A the f16 activation [T][c.cin]:
-    // a plain GEMM for kernel 1 (and the transposed conv's columns), an implicit GEMM otherwise
-    acb_status conv(const Conv & c, int64_t T, float * y, int64_t ldy, const float * bias, const float * res) {
-        if (c.kernel == 1) {
-            return acb_gemm_tc(A.p, c.Kp, c.w.p, c.Kp, T, c.N, c.Kp, y, ACB_TYPE_F32, ldy, bias, res, ldy, nullptr, 0,
-                               1, ACB_FLAG_F16, ws.p, ws.bytes, err.as<int>(), (acb_stream_t) st);
-        }
-        return acb_conv1d_tc(A.p, c.cin, T, c.cin, c.w.p, c.N, c.kernel, c.dil, (c.kernel / 2) * c.dil, y,
-                             ACB_TYPE_F32, ldy, bias, res, ldy, ACB_FLAG_F16, ws.p, ws.bytes, err.as<int>(),
-                             (acb_stream_t) st);
+    // one convolution over the f16 activation X [T][c.cin]: y [T][ldy] f32 = conv + bias (+ res)
+    acb_status conv(const Conv & c, const void * X, int64_t T, int pad, float * y, int64_t ldy, const float * bias,
+                    const float * res) {
+        return acb_conv1d_tc(X, c.cin, T, c.cin, c.w.p, c.N, c.kernel, c.dil, pad, y, ACB_TYPE_F32, ldy, bias, res,
+                             ldy, ACB_FLAG_F16, ws.p, ws.bytes, err.as<int>(), (acb_stream_t) st);
     }
 
     acb_status reserve(int64_t T0);
@@ -224,52 +226,48 @@ struct acb_vae {
 };
 
 acb_status acb_vae::reserve(int64_t T0) {
-    int64_t T = T0, mx = T0 * std::max(c1.N, 1), mA = T0 * c1.cin, mcol = 0;
-    size_t  wsb = std::max(acb_gemm_workspace_bytes(T0, c1.N, c1.Kp), (size_t) 0);
+    int64_t T = T0, mx = T0 * std::max(c1.N, latent);
+    size_t  wsb = acb_gemm_workspace_bytes(T0, c1.N, c1.Kp);
     for (const Block & b : blk) {
-        mA   = std::max(mA, T * b.ct.Kp);
-        mcol = std::max(mcol, T * (int64_t) b.ct.N);
-        wsb  = std::max(wsb, acb_gemm_workspace_bytes(T, b.ct.N, b.ct.Kp));
+        wsb = std::max(wsb, acb_gemm_workspace_bytes(T, b.ct.N, b.ct.Kp));
         T *= b.stride;
         mx = std::max(mx, T * (int64_t) b.out_ch);
         for (const ResUnit & r : b.ru) {
-            mA  = std::max({ mA, T * (int64_t) r.c1.cin, T * (int64_t) r.c2.cin });
             wsb = std::max({ wsb, acb_gemm_workspace_bytes(T, r.c1.N, r.c1.Kp),
                              acb_gemm_workspace_bytes(T, r.c2.N, r.c2.Kp) });
         }
     }
     ACB_TRY(grow(x, (size_t) mx * 4));
     ACB_TRY(grow(h, (size_t) mx * 4));
-    ACB_TRY(grow(A, (size_t) mA * 2));
-    ACB_TRY(grow(col, (size_t) mcol * 4));
+    ACB_TRY(grow(a16, (size_t) mx * 2));
     ACB_TRY(grow(ws, std::max(wsb, (size_t) 256)));
     return ACB_OK;
 }
 
 // vae_ggml_build_graph (vae.h:353-388) on device buffers: d_latent [T0][latent] f32 ->
-// d_audio [2][T0 * up] f32
+// d_audio [2][T0 * up] f32. a16 holds the f16 operand of the next conv.
 acb_status acb_vae::run(const float * d_latent, int64_t T0, float * d_audio) {
     const acb_stream_t as = (acb_stream_t) st;
     int64_t            T  = T0;
     float *            xp = x.as<float>();
     float *            hp = h.as<float>();
-    // conv1, no snake in front
-    ACB_TRY(acb_vae_snake_f16(d_latent, latent, T, latent, nullptr, nullptr, A.p, latent, as));
-    ACB_TRY(conv(c1, T, xp, c1.N, c1.b.as<float>(), nullptr));
+    void *             A  = a16.p;
+    // conv1, no snake in front: its input is the latent cast to f16
+    ACB_TRY(acb_vae_snake_f16(d_latent, latent, T, latent, nullptr, nullptr, A, latent, as));
+    ACB_TRY(conv(c1, A, T, c1.kernel / 2, xp, c1.N, c1.b.as<float>(), nullptr));
     int C = c1.N;
     for (Block & b : blk) {
-        // snake -> ConvTranspose1d: GEMM into columns, then the overlap-add with the bias
-        ACB_TRY(acb_vae_snake_f16(xp, C, T, C, b.sn.ea.as<float>(), b.sn.ib.as<float>(), A.p, C, as));
-        ACB_TRY(conv(b.ct, T, col.as<float>(), b.ct.N, nullptr, nullptr));
-        const int pad = (b.kernel - b.stride) / 2;
-        ACB_TRY(acb_vae_col2im(col.as<float>(), T, b.out_ch, b.kernel, b.stride, pad, b.ctb.as<float>(), xp, as));
+        const int64_t sN = (int64_t) b.stride * b.out_ch;
+        // snake -> ConvTranspose1d as the 3-tap phase-major convolution: [T][s*OC] = [T*s][OC]
+        ACB_TRY(acb_vae_snake_f16(xp, C, T, C, b.sn.ea.as<float>(), b.sn.ib.as<float>(), A, C, as));
+        ACB_TRY(conv(b.ct, A, T, 1, xp, sN, b.ctb.as<float>(), nullptr));
         T *= b.stride;
         C = b.out_ch;
-        for (ResUnit & r : b.ru) {
-            ACB_TRY(acb_vae_snake_f16(xp, C, T, C, r.s1.ea.as<float>(), r.s1.ib.as<float>(), A.p, C, as));
-            ACB_TRY(conv(r.c1, T, hp, C, r.c1.b.as<float>(), nullptr));
-            ACB_TRY(acb_vae_snake_f16(hp, C, T, C, r.s2.ea.as<float>(), r.s2.ib.as<float>(), A.p, C, as));
-            ACB_TRY(conv(r.c2, T, xp, C, r.c2.b.as<float>(), xp));  // + skip, in place
+        for (ResUnit & u : b.ru) {
+            ACB_TRY(acb_vae_snake_f16(xp, C, T, C, u.s1.ea.as<float>(), u.s1.ib.as<float>(), A, C, as));
+            ACB_TRY(conv(u.c1, A, T, (u.c1.kernel / 2) * u.c1.dil, hp, C, u.c1.b.as<float>(), nullptr));
+            ACB_TRY(acb_vae_snake_f16(hp, C, T, C, u.s2.ea.as<float>(), u.s2.ib.as<float>(), A, C, as));
+            ACB_TRY(conv(u.c2, A, T, 0, xp, C, u.c2.b.as<float>(), xp));  // + skip, in place
         }
     }
     return acb_vae_out_conv(xp, T, C, sn.ea.as<float>(), sn.ib.as<float>(), c2w.p, d_audio, as);
@@ -317,19 +315,36 @@ extern "C" acb_status acb_vae_load(const char * gguf_path, int device, acb_vae *
             set_last_error("VAE block " + std::to_string(i) + " shapes do not chain");
             return ACB_ERR_FORMAT;
         }
-        const std::vector<float> w = fuse_wn(g, v, IC);
-        std::vector<float>       pw((size_t) (K * OC * IC));
-        for (int64_t ic = 0; ic < IC; ic++) {
+        const std::vector<float> w = fuse_wn(g, v, IC);  // [IC][OC][K]
+        const int64_t            s = K / 2;
+        if (s % 2 != 0) {
+            set_last_error("VAE block " + std::to_string(i) + ": odd stride (the 3-tap form needs padding s/2)");
+            return ACB_ERR_UNSUPPORTED;
+        }
+        // W3[r*OC + oc][(j+1)*IC + ic] = w[ic][oc][k]: phase r takes tap k from input row q + j
+        std::vector<float> pw((size_t) (s * OC * 3 * IC), 0.0f);
+        for (int64_t r = 0; r < s; r++) {
+            const int64_t kj[3] = { r < s / 2 ? r + 3 * s / 2 : -1, r + s / 2, r >= s / 2 ? r - s / 2 : -1 };
             for (int64_t oc = 0; oc < OC; oc++) {
-                for (int64_t k = 0; k < K; k++) {
-                    pw[(size_t) ((k * OC + oc) * IC + ic)] = w[(size_t) ((ic * OC + oc) * K + k)];
+                float * row = &pw[(size_t) ((r * OC + oc) * 3 * IC)];
+                for (int j = 0; j < 3; j++) {
+                    if (kj[j] < 0) {
+                        continue;
+                    }
+                    for (int64_t ic = 0; ic < IC; ic++) {
+                        row[j * IC + ic] = w[(size_t) ((ic * OC + oc) * K + kj[j])];
+                    }
                 }
             }
         }
-        b.in_ch = (int) IC, b.out_ch = (int) OC, b.kernel = (int) K, b.stride = (int) K / 2;
-        b.ct.N = (int) (K * OC), b.ct.Kp = (int) IC, b.ct.cin = (int) IC, b.ct.kernel = 1;
+        b.in_ch = (int) IC, b.out_ch = (int) OC, b.kernel = (int) K, b.stride = (int) s;
+        b.ct.N = (int) (s * OC), b.ct.Kp = (int) (3 * IC), b.ct.cin = (int) IC, b.ct.kernel = 3, b.ct.dil = 1;
         ACB_TRY(upload_f16(b.ct.w, pw, tmp));
-        ACB_TRY(upload_f32(b.ctb, bias));
+        std::vector<float> tb((size_t) (s * OC));
+        for (int64_t r = 0; r < s; r++) {
+            std::copy(bias.begin(), bias.end(), tb.begin() + r * OC);
+        }
+        ACB_TRY(upload_f32(b.ctb, tb));
         C = (int) OC;
         m->up *= b.stride;
         for (int r = 0; r < 3; r++) {
@@ -374,7 +389,7 @@ extern "C" acb_status acb_vae_load(const char * gguf_path, int device, acb_vae *
     m->c_last = C;
     // every conv's input channel count must be a multiple of 64 (one k-tile of the GEMM holds one
     // 64-channel slice of one tap): the shipped channel counts are multiples of 128
-    bool ok = C % 8 == 0 && m->c1.cin % 64 == 0;
+    bool ok = C % 8 == 0 && m->c1.cin % 64 == 0 && m->c1.N % 8 == 0;
     for (const Block & b : m->blk) {
         ok = ok && b.ct.cin % 64 == 0 && b.out_ch % 8 == 0;
         for (const ResUnit & r : b.ru) {

@@ -299,9 +299,9 @@ ACB_API acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int6
  * mul_mat, src/vae.h:283-297, without the im2col buffer):
  *   Y[t][n] = epi( sum_{k, c} X[t + k*dilation - pad][c] * W[n][k*C_in + c] ),
  * X [T][ldx] bf16 / f16 (ACB_FLAG_F16) rows of C_in channels, rows outside [0, T) read as 0 (the
- * TMA bounds fill), W [N][kernel*C_in] in the same type, stride 1, T_out = T when
- * 2*pad = (kernel-1)*dilation. Epilogue, workspace, flags and Y types as acb_gemm_tc. C_in a
- * multiple of 64 (one 64-channel slice of one tap per k-tile). */
+ * TMA bounds fill), W [N][kernel*C_in] in the same type, stride 1 (T_out = T when 2*pad =
+ * (kernel-1)*dilation). Epilogue, workspace, flags and Y types as acb_gemm_tc. C_in a multiple of
+ * 64 (one 64-channel slice of one tap per k-tile). */
 ACB_API acb_status acb_conv1d_tc(const void * X, int64_t ldx, int64_t T, int C_in, const void * W, int64_t N,
                                  int kernel, int dilation, int pad, void * Y, int y_type, int64_t ldy,
                                  const float * bias, const float * res, int64_t ldr, int flags, void * workspace,
@@ -443,10 +443,6 @@ ACB_API acb_status acb_rows_prepend(const float * head, const float * src, int64
  * multiples of 8, x and y 16-byte aligned. */
 ACB_API acb_status acb_vae_snake_f16(const float * x, int64_t x_stride, int64_t T, int C, const float * exp_alpha,
                                      const float * inv_beta, void * y, int64_t ldy, acb_stream_t stream);
-/* ConvTranspose1d overlap-add: col [T_in][kernel*OC] (column k*OC + oc of input step t_in) ->
- * y [T_out][OC], T_out = (T_in - 1)*stride + kernel - 2*pad, plus bias (NULL: none). */
-ACB_API acb_status acb_vae_col2im(const float * col, int64_t T_in, int OC, int kernel, int stride, int pad,
-                                  const float * bias, float * y, acb_stream_t stream);
 /* The output conv: snake, then C -> 2 channels, kernel 7, pad 3, no bias; w f16 [2][7][C];
  * y planar [2][T]. */
 ACB_API acb_status acb_vae_out_conv(const float * x, int64_t T, int C, const float * exp_alpha,
