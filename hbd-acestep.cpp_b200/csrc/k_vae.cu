@@ -41,62 +41,75 @@ __global__ void snake_f16_kernel(const float * __restrict__ x, int64_t xs, int64
 }
 
 // Final conv, C channels -> 2, k = 7, pad 3, with the snake. A CTA of 8 warps covers 128 samples:
-// the snake'd f16 inputs of samples [t0 - 3, t0 + 131) and the f16 weights are staged in shared
-// memory once; a warp computes one sample at a time with its lanes across channel quads
-// (consecutive 8-byte reads, no bank conflicts), f32 products and sums, reduced over the lanes.
+// the snake'd inputs of samples [t0 - 3, t0 + 131), rounded to f16 (the conv's operand type) and
+// kept as f32, are staged in shared memory once; a warp computes one sample at a time with its
+// lanes across channel quads (one 16-byte shared read per tap, no bank conflicts), f32 products
+// and sums, reduced over the lanes. With C <= 128 every lane holds its quads' 14 weight vectors
+// in registers (REGW); wider layers read them from shared memory.
 constexpr int kOutTile = 128, kOutThreads = 256;
 
+template <bool REGW>
 __global__ void __launch_bounds__(kOutThreads) out_conv_kernel(const float * __restrict__ x, int64_t T, int C,
                                                                const float * __restrict__ ea,
                                                                const float * __restrict__ ib,
                                                                const __half * __restrict__ w,  // [2][7][C]
                                                                float * __restrict__ y) {
-    extern __shared__ __align__(16) __half os_smem[];  // [kOutTile + 6][C] inputs, [14][C] weights
-    __half *      xs = os_smem;
-    __half *      wsm = os_smem + (kOutTile + 6) * C;
+    extern __shared__ __align__(16) float oc_smem[];  // [kOutTile + 6][C] inputs, [14][C] weights
+    float *          xs  = oc_smem;
+    float *          wsm = oc_smem + (kOutTile + 6) * C;
     __shared__ float res[2][kOutTile];
-    const int64_t t0 = (int64_t) blockIdx.x * kOutTile;
-    const int     cq = C / 4;
+    const int64_t    t0 = (int64_t) blockIdx.x * kOutTile;
+    const int        cq = C / 4;
     for (int i = threadIdx.x; i < (kOutTile + 6) * cq; i += blockDim.x) {
         const int     r  = i / cq, c = (i - r * cq) * 4;
         const int64_t ts = t0 - 3 + r;
-        union {
-            uint2  u;
-            __half h[4];
-        } o;
+        float4        o  = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (ts >= 0 && ts < T) {
             const float4 v = *reinterpret_cast<const float4 *>(x + ts * C + c);
-            o.h[0]         = __float2half_rn(snake_f(v.x, __ldg(ea + c), __ldg(ib + c)));
-            o.h[1]         = __float2half_rn(snake_f(v.y, __ldg(ea + c + 1), __ldg(ib + c + 1)));
-            o.h[2]         = __float2half_rn(snake_f(v.z, __ldg(ea + c + 2), __ldg(ib + c + 2)));
-            o.h[3]         = __float2half_rn(snake_f(v.w, __ldg(ea + c + 3), __ldg(ib + c + 3)));
-        } else {
-            o.u = make_uint2(0, 0);
+            o.x            = __half2float(__float2half_rn(snake_f(v.x, __ldg(ea + c), __ldg(ib + c))));
+            o.y            = __half2float(__float2half_rn(snake_f(v.y, __ldg(ea + c + 1), __ldg(ib + c + 1))));
+            o.z            = __half2float(__float2half_rn(snake_f(v.z, __ldg(ea + c + 2), __ldg(ib + c + 2))));
+            o.w            = __half2float(__float2half_rn(snake_f(v.w, __ldg(ea + c + 3), __ldg(ib + c + 3))));
         }
-        *reinterpret_cast<uint2 *>(xs + r * C + c) = o.u;
+        *reinterpret_cast<float4 *>(xs + r * C + c) = o;
     }
-    for (int i = threadIdx.x; i < 14 * cq; i += blockDim.x) {
-        *reinterpret_cast<uint2 *>(wsm + i * 4) = *reinterpret_cast<const uint2 *>(w + i * 4);
+    for (int i = threadIdx.x; i < 14 * C; i += blockDim.x) {
+        wsm[i] = __half2float(w[i]);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float4    wr[14];  // REGW: this lane's quad (lane) of the 2 x 7 weight rows
+    if constexpr (REGW) {
+#pragma unroll
+        for (int j = 0; j < 14; j++) {
+            wr[j] = lane < cq ? *reinterpret_cast<const float4 *>(wsm + j * C + 4 * lane) : make_float4(0, 0, 0, 0);
+        }
+    }
     for (int s = warp; s < kOutTile; s += kOutThreads / 32) {
         float a0 = 0.0f, a1 = 0.0f;
+        if constexpr (REGW) {
+            if (lane < cq) {
 #pragma unroll
-        for (int k = 0; k < 7; k++) {
-            for (int q = lane; q < cq; q += 32) {
-                union {
-                    uint2  u;
-                    __half h[4];
-                } xv, w0, w1;
-                xv.u = *reinterpret_cast<const uint2 *>(xs + (s + k) * C + 4 * q);
-                w0.u = *reinterpret_cast<const uint2 *>(wsm + k * C + 4 * q);
-                w1.u = *reinterpret_cast<const uint2 *>(wsm + (7 + k) * C + 4 * q);
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float xf = __half2float(xv.h[e]);
-                    a0             = fmaf(xf, __half2float(w0.h[e]), a0);
-                    a1             = fmaf(xf, __half2float(w1.h[e]), a1);
+                for (int k = 0; k < 7; k++) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(xs + (s + k) * C + 4 * lane);
+                    a0 = fmaf(xv.x, wr[k].x, a0);
+                    a0 = fmaf(xv.y, wr[k].y, a0);
+                    a0 = fmaf(xv.z, wr[k].z, a0);
+                    a0 = fmaf(xv.w, wr[k].w, a0);
+                    a1 = fmaf(xv.x, wr[7 + k].x, a1);
+                    a1 = fmaf(xv.y, wr[7 + k].y, a1);
+                    a1 = fmaf(xv.z, wr[7 + k].z, a1);
+                    a1 = fmaf(xv.w, wr[7 + k].w, a1);
+                }
+            }
+        } else {
+            for (int k = 0; k < 7; k++) {
+                for (int q = lane; q < cq; q += 32) {
+                    const float4 xv = *reinterpret_cast<const float4 *>(xs + (s + k) * C + 4 * q);
+                    const float4 w0 = *reinterpret_cast<const float4 *>(wsm + k * C + 4 * q);
+                    const float4 w1 = *reinterpret_cast<const float4 *>(wsm + (7 + k) * C + 4 * q);
+                    a0              = fmaf(xv.x, w0.x, fmaf(xv.y, w0.y, fmaf(xv.z, w0.z, fmaf(xv.w, w0.w, a0))));
+                    a1              = fmaf(xv.x, w1.x, fmaf(xv.y, w1.y, fmaf(xv.z, w1.z, fmaf(xv.w, w1.w, a1))));
                 }
             }
         }
@@ -145,14 +158,17 @@ extern "C" acb_status acb_vae_out_conv(const float * x, int64_t T, int C, const 
     if (!x || !w || !y || !exp_alpha || !inv_beta || T <= 0 || C <= 0) {
         return ACB_ERR_INVALID_ARG;
     }
-    const size_t smem = (size_t) (kOutTile + 6 + 14) * C * 2;
-    if (C % 4 || smem > 200 * 1024 || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 7)) {
+    const size_t smem = (size_t) (kOutTile + 6 + 14) * C * 4;
+    if (C % 4 || smem > 200 * 1024 || (reinterpret_cast<uintptr_t>(x) & 15)) {
         return ACB_ERR_UNSUPPORTED;
     }
+    const bool regw = C <= 128;
+    void (*kern)(const float *, int64_t, int, const float *, const float *, const __half *, float *) =
+        regw ? out_conv_kernel<true> : out_conv_kernel<false>;
     if (smem > 48 * 1024) {
-        cudaFuncSetAttribute(out_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem);
     }
-    out_conv_kernel<<<(unsigned) ((T + kOutTile - 1) / kOutTile), kOutThreads, smem, (cudaStream_t) stream>>>(
+    kern<<<(unsigned) ((T + kOutTile - 1) / kOutTile), kOutThreads, smem, (cudaStream_t) stream>>>(
         x, T, C, exp_alpha, inv_beta, reinterpret_cast<const __half *>(w), y);
     return launch_status();
 }
