@@ -116,7 +116,7 @@ __device__ __forceinline__ float silu_times(float g, float u) {
     return __fmul_rn(s, u);
 }
 
-// The VAE's snake activation x + sin(x * e^a)^2 * e^-b (src/vae.h:270-280, ggml_mul, ggml_sin,
+// The VAE's snake activation x + sin(x * e^a)^2 * e^-b (src/vae.h:267-276, ggml_mul, ggml_sin,
 // ggml_sqr, ggml_mul, ggml_add: each node rounded once); ea = e^a, ib = e^-b per channel. One
 // definition for the standalone kernel and the GEMM epilogue that fuses it.
 __device__ __forceinline__ float snake_f(float x, float ea, float ib) {

@@ -1,10 +1,10 @@
-// k_vae.cu -- the AutoencoderOobleck decoder's non-GEMM ops (src/vae.h:270-364). Its convolutions
+// k_vae.cu -- the AutoencoderOobleck decoder's non-GEMM ops (src/vae.h:267-369). Its convolutions
 // run on the tensor-core GEMM (acb_conv1d_tc, an implicit GEMM: TMA reads each tap's rows of the
 // f16 activation directly, with zero fill outside [0, T)), whose epilogue also applies the next
 // snake; what remains here:
 //
 //   acb_vae_snake_f16     y[t][c] = f16(snake(x[t][c])): the snake activation x + sin(x*e^a)^2 *
-//                         e^-b (vae_snake, :270-280, five separately rounded f32 ops), rounded to
+//                         e^-b (vae_snake, :267-276, five separately rounded f32 ops), rounded to
 //                         the f16 operand type ggml_conv_1d gives the activation (its im2col takes
 //                         the weights' type). Without e^a a plain cast (the first conv's input).
 //   acb_vae_out_conv      the last conv (C -> 2 channels, k = 7, no bias) with its snake, as a

@@ -102,7 +102,7 @@ bool read_f32(const GGUFFile & gf, const std::string & name, std::vector<float> 
     return true;
 }
 
-// weight_norm over dim 0 (vae_fuse_wn, vae.h:63-91): w[d][i] = v[d][i] * g[d] / (|v[d]| + 1e-12),
+// weight_norm over dim 0 (vae_fuse_wn, vae.h:64-93; vae_fuse_wn_ct, :100-128): w[d][i] = v[d][i] * g[d] / (|v[d]| + 1e-12),
 // the norm from a sequential f32 sum of squares
 std::vector<float> fuse_wn(const std::vector<float> & g, const std::vector<float> & v, int64_t dim0) {
     const int64_t      fan = (int64_t) v.size() / dim0;
@@ -145,7 +145,7 @@ acb_status load_snake(const GGUFFile & gf, const std::string & pfx, Snake & s, i
     if (!read_f32(gf, pfx + ".alpha", a) || !read_f32(gf, pfx + ".beta", b) || a.size() != b.size()) {
         return ACB_ERR_FORMAT;
     }
-    for (size_t i = 0; i < a.size(); i++) {  // vae_load_snake / vae_load_snake_inv (:101-125)
+    for (size_t i = 0; i < a.size(); i++) {  // vae_load_snake / vae_load_snake_inv (:131-152)
         a[i] = expf(a[i]);
         b[i] = 1.0f / expf(b[i]);
     }
@@ -244,7 +244,7 @@ acb_status acb_vae::reserve(int64_t T0) {
     return ACB_OK;
 }
 
-// vae_ggml_build_graph (vae.h:353-388) on device buffers: d_latent [T0][latent] f32 ->
+// vae_ggml_build_graph (vae.h:344-369) on device buffers: d_latent [T0][latent] f32 ->
 // d_audio [2][T0 * up] f32. a16 holds the f16 operand of the next conv.
 acb_status acb_vae::run(const float * d_latent, int64_t T0, float * d_audio) {
     const acb_stream_t as = (acb_stream_t) st;
@@ -421,7 +421,7 @@ extern "C" acb_status acb_vae_decode_device(acb_vae * m, const float * d_latent,
     return cudaStreamSynchronize(m->st) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
 }
 
-// vae_ggml_decode (vae.h:466-488): host latent [T][latent] -> host audio [2][T * up]
+// vae_ggml_decode (vae.h:442-459): host latent [T][latent] -> host audio [2][T * up]
 extern "C" acb_status acb_vae_decode(acb_vae * m, const float * latent, int T_latent, float * audio_out,
                                      int max_T_audio, int * out_T_audio) {
     if (!m || !latent || !audio_out || T_latent <= 0) {
@@ -464,7 +464,7 @@ extern "C" acb_status acb_vae_decode(acb_vae * m, const float * latent, int T_la
     return ACB_OK;
 }
 
-// vae_ggml_decode_tiled (vae.h:495-585): windows of chunk_size latent frames with `overlap`
+// vae_ggml_decode_tiled (vae.h:467-565): windows of chunk_size latent frames with `overlap`
 // frames of context on each side, each decoded on its own and trimmed to its core, cores
 // concatenated; audio_out holds channel 0 for T_audio samples, then channel 1.
 extern "C" acb_status acb_vae_decode_tiled(acb_vae * m, const float * latent, int T_latent, float * audio_out,

@@ -326,7 +326,7 @@ VAE_TINY = dict(latent=64, c0=256, in_ch=[256, 128, 128, 64, 64], out_ch=[128, 1
 
 def vae_tensors(vcfg: dict, seed: int = 0):
     """Yields (name, numpy float32 array in PyTorch shape) of an AutoencoderOobleck decoder with the
-    reference's GGUF names (vae.h:200-240): weight-normalised convs (weight_g [OC,1,1], weight_v),
+    reference's GGUF names (vae.h:229-255): weight-normalised convs (weight_g [OC,1,1], weight_v),
     biases, snake alpha / beta [1, C, 1]. Stored BF16 by write_vae_gguf, as convert.py does.
     Conditioned like a trained residual decoder, so that rounding differences stay small at the
     output: residual branches end in a small gain (conv2 weight_g 0.1-0.3) and the snake's

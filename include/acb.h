@@ -296,7 +296,7 @@ ACB_API acb_status acb_gemm_tc(const void * A, int64_t lda, const void * B, int6
                                acb_stream_t stream);
 
 /* 1-D convolution as an implicit GEMM on the same tensor-core kernel (ggml_conv_1d = im2col +
- * mul_mat, src/vae.h:283-297, without the im2col buffer):
+ * mul_mat, src/vae.h:279-295, without the im2col buffer):
  *   Y[t][n] = epi( sum_{k, c} X[t + k*dilation - pad][c] * W[n][k*C_in + c] ),
  * X [T][ldx] bf16 / f16 (ACB_FLAG_F16) rows of C_in channels, rows outside [0, T) read as 0 (the
  * TMA bounds fill), W [N][kernel*C_in] in the same type, stride 1 (T_out = T when 2*pad =
@@ -437,7 +437,7 @@ ACB_API acb_status acb_rows_prepend(const float * head, const float * src, int64
 /* ---- VAE decoder ops (src/vae.h) -------------------------------------------------------------- */
 
 /* y [T][ldy] f16 = f16(snake(x)) with the snake x + sin(x*e^a)^2 * e^-b (vae_snake, src/vae.h:
- * 270-280: exp_alpha = e^a, inv_beta = e^-b per channel, five separately rounded f32 ops; NULL:
+ * 267-276: exp_alpha = e^a, inv_beta = e^-b per channel, five separately rounded f32 ops; NULL:
  * no snake, a plain cast). f16 is the operand type ggml_conv_1d gives the activation (its im2col
  * takes the f16 weights' type); acb_conv1d_tc reads y in place of the im2col. C, x_stride, ldy
  * multiples of 8, x and y 16-byte aligned. */

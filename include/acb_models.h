@@ -15,7 +15,7 @@ extern "C" {
 #endif
 
 /* Cancellation callback, polled between steps of a long call (denoise steps, dit-sampler.h:409-413;
- * VAE tiles, vae.h:536): nonzero stops the call with ACB_ERR_CANCELLED. */
+ * VAE tiles, vae.h:496): nonzero stops the call with ACB_ERR_CANCELLED. */
 typedef int (*acb_cancel_fn)(void * data);
 
 /* ---- GGUF (replaces gf_load / gf_close / gf_get_*, src/gguf-weights.h:48-155,357-390) ---- */
@@ -141,19 +141,19 @@ ACB_API void       acb_cond_free(acb_cond * m); /* cond_ggml_free :383 */
 
 typedef struct acb_vae acb_vae;
 
-/* vae_ggml_load (vae.h:128-250): decoder.* of an acestep-vae GGUF (BF16 weight_g / weight_v,
+/* vae_ggml_load (vae.h:167-259): decoder.* of an acestep-vae GGUF (BF16 weight_g / weight_v,
  * biases, snake alpha / beta). Weight normalisation is fused at load as the reference does it and
  * the weights kept in f16; channels and strides come from the tensor shapes (channel counts must
  * be multiples of 64). */
 ACB_API acb_status acb_vae_load(const char * gguf_path, int device, acb_vae ** out);
 ACB_API int        acb_vae_upsample(const acb_vae * m); /* audio samples per latent frame (1920) */
-/* vae_ggml_decode (vae.h:466-488): latent [T_latent][64] (host, time-major as the DiT writes it)
+/* vae_ggml_decode (vae.h:442-459): latent [T_latent][64] (host, time-major as the DiT writes it)
  * -> audio_out [2][T_audio] (host: channel 0 then channel 1), T_audio = T_latent * upsample <=
  * max_T_audio. Convolutions run as tcgen05 GEMMs on f16 operands (ggml's conv_1d casts the
  * activation to the f16 weights), snake activations in f32. */
 ACB_API acb_status acb_vae_decode(acb_vae * m, const float * latent, int T_latent, float * audio_out,
                                   int max_T_audio, int * out_T_audio);
-/* vae_ggml_decode_tiled (vae.h:495-585): the same windows (chunk_size frames plus overlap of
+/* vae_ggml_decode_tiled (vae.h:467-565): the same windows (chunk_size frames plus overlap of
  * context each side, reference defaults 256 / 64), trims and layout; cancel is polled per tile. */
 ACB_API acb_status acb_vae_decode_tiled(acb_vae * m, const float * latent, int T_latent, float * audio_out,
                                         int max_T_audio, int chunk_size, int overlap, acb_cancel_fn cancel,

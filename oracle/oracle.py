@@ -1030,9 +1030,9 @@ def lora_merge(entry, A, B, scaling):
 # ---- VAE decoder (src/vae.h) ----------------------------------------------------------------------
 
 class OracleVAE:
-    """vae_ggml_load + vae_ggml_build_graph (src/vae.h:128-388) in numpy over the GGUF's bf16 bits
+    """vae_ggml_load + vae_ggml_build_graph (src/vae.h:167-369) in numpy over the GGUF's bf16 bits
     {name: uint16 array in PyTorch shape}: weight norm fused in f32 with a sequential sum of squares
-    (vae_fuse_wn, :63-91) and rounded to f16; snake in f32 (five separately rounded ops); every conv
+    (vae_fuse_wn, :64-93) and rounded to f16; snake in f32 (five separately rounded ops); every conv
     as an im2col of f16-cast activations times the f16 weights, exact products summed in float64
     and rounded to f32 (ggml_conv_1d's operand types; the sum order of ggml is not reproduced);
     ConvTranspose as that GEMM plus the overlap-add in ascending kernel tap, then the bias."""
@@ -1131,7 +1131,7 @@ class OracleVAE:
         return np.ascontiguousarray(y.T)
 
     def decode_tiled(self, latent, chunk_size=256, overlap=64):
-        """vae_ggml_decode_tiled (src/vae.h:495-585) over decode()."""
+        """vae_ggml_decode_tiled (src/vae.h:467-565) over decode()."""
         T = latent.shape[0]
         while chunk_size - 2 * overlap <= 0 and overlap > 0:
             overlap //= 2

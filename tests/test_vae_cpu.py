@@ -1,4 +1,4 @@
-"""CPU: the oracle's VAE decoder restatement (src/vae.h:63-388) pinned against PyTorch's own
+"""CPU: the oracle's VAE decoder restatement (src/vae.h:64-369) pinned against PyTorch's own
 definition of the AutoencoderOobleck decoder: torch.nn.functional conv1d / conv_transpose1d and
 the weight_norm formula g * v / |v| in float64, with the reference's operand precision applied
 (f16 weights, f16-cast conv inputs). This checks the oracle's padding, dilation, stride, crop,

@@ -50,7 +50,7 @@ def test_vae_decode_tiled_tiny(tiny):
     got = vae.decode_tiled(lat, chunk_size=8, overlap=2)
     ref = ov.decode_tiled(lat, chunk_size=8, overlap=2)
     _close(got, ref, "tiled")
-    # overlap larger than half the chunk is halved until a core remains (vae.h:503-505)
+    # overlap larger than half the chunk is halved until a core remains (vae.h:477-479)
     _close(vae.decode_tiled(lat, chunk_size=6, overlap=4), ov.decode_tiled(lat, chunk_size=6, overlap=4), "halved")
 
 
