@@ -146,6 +146,7 @@ def lib():
             "acb_gemm_workspace_bytes": (C.c_size_t, [I64, I64, I64]),
             "acb_conv1d_tc": (I, [P, I64, I64, I, P, I64, I, I, I, P, I, I64, P, P, I64, I, P, C.c_size_t, P, P]),
             "acb_vae_snake_f16": (I, [P, I64, I64, I, P, P, P, I64, P]),
+            "acb_stream_wait_flag": (I, [P, C.c_uint32, C.c_uint64, P, P]),
             "acb_vae_out_conv": (I, [P, I64, I, P, P, P, P, P]),
             "acb_gemm_swiglu_quant": (I, [P, I64, P, I64, I64, I64, I64, P, I, I, P, I, I64, I, P, P]),
             "acb_gemm_qkv_planes": (I, [P, I64, P, I64, I64, I64, I, I, P, P, F, P, P, I, I64, P, I64, I64, P, I64, I64,

@@ -147,17 +147,6 @@ __device__ __forceinline__ void cons_sync() {
     asm volatile("bar.sync 1, %0;" ::"r"(kPdCons) : "memory");
 }
 
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ unsigned ld_acquire(const unsigned * p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 __device__ __forceinline__ float f16r(float v) {
     return __half2float(__float2half_rn(v));
@@ -322,20 +311,15 @@ __device__ bool pd_grid_sync(const PdParams & P, PdCtx & x) {
         __threadfence();
         unsigned v = *sm_abort() ? (atomicOr(P.bar, kAbortBit) | kAbortBit) : atomicAdd(P.bar, 1u) + 1u;
         if (!(v & kAbortBit) && v < target) {
-            const uint64_t t0 = globaltimer();
-            for (;;) {
-                v = ld_acquire(P.bar);
-                if ((v & kAbortBit) || (v & ~kAbortBit) >= target) {
-                    break;
+            const bool done = ptx::poll_bounded<false>(
+                P.bar, kBarrierNs, [target](unsigned w) { return (w & kAbortBit) || (w & ~kAbortBit) >= target; },
+                v);
+            if (!done) {
+                if (P.s.err) {
+                    atomicOr(P.s.err, ACB_DEVERR_TIMEOUT);
                 }
-                if (globaltimer() - t0 > kBarrierNs) {
-                    if (P.s.err) {
-                        atomicOr(P.s.err, ACB_DEVERR_TIMEOUT);
-                    }
-                    atomicOr(P.bar, kAbortBit);
-                    v |= kAbortBit;
-                    break;
-                }
+                atomicOr(P.bar, kAbortBit);
+                v |= kAbortBit;
             }
         }
         if (v & kAbortBit) {

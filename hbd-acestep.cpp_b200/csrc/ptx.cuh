@@ -98,5 +98,42 @@ __device__ __forceinline__ void grid_dep_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- bounded polling of a word in global memory ----------------------------------------------
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// system scope: also sees stores of the host (mapped pinned memory) and of peer GPUs
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned * p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Re-reads *word with acquire loads (system scope when SYS) until done(value) holds or limit_ns
+// of global time have passed. Returns true when done held; v is the last value read either way.
+// Every spin-wait on another agent in this library goes through here, so none can run forever.
+template <bool SYS, class Done>
+__device__ __forceinline__ bool poll_bounded(const unsigned * word, uint64_t limit_ns, Done done, unsigned & v) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        v = SYS ? ld_acquire_sys(word) : ld_acquire_gpu(word);
+        if (done(v)) {
+            return true;
+        }
+        if (globaltimer_ns() - t0 > limit_ns) {
+            return false;
+        }
+    }
+}
+
 }  // namespace ptx
 }  // namespace acb

@@ -639,6 +639,19 @@ ACB_API size_t acb_lm_decode_scratch_bytes(const acb_decode_step * step);
  * After a step that raised a device error the scratch must be zeroed again. */
 ACB_API acb_status acb_lm_decode_step(const acb_decode_step * step, acb_stream_t stream);
 
+/* ---- bounded device-side wait ---------------------------------------------------------------
+ * Holds `stream` on the device until the 32-bit word at `flag` is >= `value` (unsigned compare,
+ * system-scope acquire loads), so later work on the stream sees what the producer wrote before
+ * raising it. The producer can be the host (a flag in mapped pinned memory), a peer GPU (P2P /
+ * IPC memory) or work on another stream that is already running; never a kernel that could be
+ * scheduled only after this one on the same GPU. After limit_ns nanoseconds (1 ns .. 10 s) of
+ * waiting it gives up: ACB_DEVERR_TIMEOUT is OR-ed into *err_flag (may be NULL), the stream goes
+ * on and the context stays usable, so a producer that never comes is reported instead of hanging
+ * the GPU. It is the same bounded poll as the persistent decode step's grid barrier. No
+ * counterpart in the reference. */
+ACB_API acb_status acb_stream_wait_flag(const uint32_t * flag, uint32_t value, uint64_t limit_ns, int * err_flag,
+                                        acb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
