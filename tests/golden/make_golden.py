@@ -107,8 +107,11 @@ def make_lm(rng, reference: str) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("ACB_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("ACB_REFERENCE"),
+                    help="checkout of the reference project (or set ACB_REFERENCE)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give the reference checkout with --reference or ACB_REFERENCE")
     rng = np.random.default_rng(20261201)
     np.savez_compressed(os.path.join(HERE, "quant_golden.npz"), **make_quant(rng))
     np.savez_compressed(os.path.join(HERE, "lm_golden.npz"), **make_lm(rng, a.reference))
