@@ -495,6 +495,12 @@ def run_ours(args):
             print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands (Q8_0-quantised activations)")),
                   flush=True)
         return
+    if args.workloads == "ditlog":
+        r = run_dit_logged(dev, rank)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 hi/lo operands, fp32 accumulation")),
+                  flush=True)
+        return
     if args.workloads == "vae":
         r = run_vae(dev, rank, want_cpu=not args.no_cpu_baseline)
         if rank == 0:
@@ -542,6 +548,9 @@ def run_ours(args):
             if "vae" in wl:
                 torch.cuda.empty_cache()
                 line["vae_decode"] = run_vae(dev, rank, want_cpu=not args.no_cpu_baseline)
+            if "ditlog" in wl:
+                torch.cuda.empty_cache()
+                line["dit_logged_case"] = run_dit_logged(dev, rank)
         if "lm5" in wl:
             # config 5's LM shards one sequence per GPU: run at every N (all ranks take part)
             torch.cuda.empty_cache()
@@ -1239,6 +1248,54 @@ def run_vae(dev, rank, want_cpu=True, T=VAE_T, reps=10):
 DIT_TRACKS, DIT_T, DIT_ENC_S, DIT_STEPS, DIT_GUIDANCE = 4, 1500, 512, 8, 3.0
 
 
+def run_dit_logged(dev, rank, reps=5):
+    """The DiT generation the reference logs on its own GPU (tests/CUDA0-Q8_0.log:156-205): one
+    track, T = 2170 latent frames (1085 tokens), enc_S = 238, the turbo model's 8 Euler steps at
+    shift 3 with guidance 1.0 (no CFG: pipeline-synth.cpp:236-261), Q8_0 weights; 268.2 ms there on
+    an RTX PRO 6000. Timed here through acb_dit_generate_ex (dit_ggml_generate's call: host noise,
+    context and condition in, host latents out) and by the library's own device clock."""
+    import tempfile
+
+    import numpy as np
+
+    import acb
+    import synthetic
+
+    cfg = dict(synthetic.ACESTEP_DIT_2B)
+    T, enc_S, Oc = 2170, 238, cfg["out_channels"]
+    path = os.path.join(tempfile.gettempdir(), f"acb_bench_ditlog_r{rank}.gguf")
+    synthetic.write_dit_gguf(path, cfg, synthetic.Q8_0, seed=21, device=str(dev))
+    dit = acb.DiT(path, device=dev.index or 0)
+    os.remove(path)
+    rng = np.random.default_rng(42)
+    noise = rng.standard_normal((1, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((1, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    enc = rng.standard_normal((1, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    sched = acb.turbo_schedule(8, 3.0)
+    for _ in range(2):
+        dit.generate_ex(noise, ctx, enc, sched, guidance_scale=1.0)
+    wall, dev_ms = [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        out, ms = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=1.0)
+        wall.append((time.perf_counter() - t0) * 1e3)
+        dev_ms.append(ms)
+    dit.close()
+    e2e_ms, gpu_ms = float(np.median(wall)), float(np.median(dev_ms))
+    return {
+        "metric": "DiT generation ms (the reference's logged case: 1 track, 1085 tokens, enc_S 238, turbo 8 steps)",
+        "value": round(gpu_ms, 2), "unit": "ms", "higher_is_better": False,
+        "config": {"workload": "dit_logged_case", "tracks": 1, "frames": T, "tokens": T // 2, "enc_rows": enc_S,
+                   "steps": 8, "shift": 3.0, "guidance": 1.0, "weights": "Q8_0 (synthetic)", "mode": "exact"},
+        "e2e": {"value": round(e2e_ms, 2), "unit": "ms", "path": "acb_dit_generate_ex",
+                "h2d_bytes_per_step": int(noise.nbytes + ctx.nbytes + enc.nbytes),
+                "d2h_bytes_per_step": int(out.nbytes)},
+        "reference_published": "268.2 ms on an RTX PRO 6000, ggml-CUDA, Q8_0 (tests/CUDA0-Q8_0.log:205; "
+                               "other hardware, context only)",
+        "x0_finite": bool(np.isfinite(out).all()),
+    }
+
+
 def dit_step_flops(cfg, Ng, S, enc_S) -> int:
     """Algorithmic FLOPs of one DiT evaluation over Ng sequences: every linear (2*rows*N*K; the
     condition K/V projections counted once per step as the reference computes them) plus self
@@ -1732,13 +1789,14 @@ def main():
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
     ap.add_argument("--lm5-gen", type=int, default=LM5_GEN, help="config 5 LM tokens (profiling runs use fewer)")
-    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,lm5,dit5",
+    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,ditlog,lm5,dit5",
                     help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
-                         "decode), enc (config 1 text encoder), vae (the audio decoder on 86.8 s) -- those four at "
+                         "decode), enc (config 1 text encoder), vae (the audio decoder on 86.8 s), ditlog (the DiT "
+                         "generation the reference logs: 1 track, turbo, no CFG) -- those five at "
                          "N=1 as sub-results -- and lm5 "
                          "(config 5's 4B Q4_K_M LM, one sequence per GPU, at every N), dit5 (config 5's DiT leg, "
                          "track pairs per GPU, at every N); without dit, ops is the "
-                         "headline; or one of gemv / gemm / enc / vae / ditmodes / lm5 alone")
+                         "headline; or one of gemv / gemm / enc / vae / ditlog / ditmodes / lm5 alone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
