@@ -495,6 +495,12 @@ def run_ours(args):
             print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands (Q8_0-quantised activations)")),
                   flush=True)
         return
+    if args.workloads == "condlog":
+        r = run_cond_logged(dev, rank)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 hi/lo operands, fp32 accumulation")),
+                  flush=True)
+        return
     if args.workloads == "ditlog":
         r = run_dit_logged(dev, rank)
         if rank == 0:
@@ -551,6 +557,9 @@ def run_ours(args):
             if "ditlog" in wl:
                 torch.cuda.empty_cache()
                 line["dit_logged_case"] = run_dit_logged(dev, rank)
+            if "condlog" in wl:
+                torch.cuda.empty_cache()
+                line["cond_logged_case"] = run_cond_logged(dev, rank)
         if "lm5" in wl:
             # config 5's LM shards one sequence per GPU: run at every N (all ranks take part)
             torch.cuda.empty_cache()
@@ -1152,6 +1161,64 @@ def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
 # latent frames: 86.8 s of 48 kHz stereo audio (1920 samples per frame), the length the reference
 # logs its tiled decode at (tests/CUDA0-Q8_0.log:216-222: 3 tiles of chunk 1024 / overlap 64)
 VAE_T = 2170
+
+
+def run_cond_logged(dev, rank, reps=10):
+    """The conditioning the reference logs on its own GPU (tests/CUDA0-Q8_0.log:406-433): the BF16
+    Qwen3-0.6B text encoder on 70 caption tokens, the lyric embedding lookup of 167 tokens, and the
+    Q8_0 condition encoder (lyric 8 layers with the 128 sliding window, timbre 4 layers on one
+    reference row, text projection) packed into enc_S = 238 rows; 15.9 ms warm there on an RTX PRO
+    6000. Timed here as the three host calls of acb_qwen3_forward, acb_qwen3_embed_lookup and
+    acb_cond_forward (host buffers in and out)."""
+    import tempfile
+
+    import numpy as np
+
+    import acb
+    import synthetic
+
+    tcfg = dict(synthetic.QWEN3_EMBED_0_6B)
+    tpath = os.path.join(tempfile.gettempdir(), f"acb_bench_textenc_bf16_r{rank}.gguf")
+    synthetic.write_lm_gguf(tpath, tcfg, synthetic.policy_bf16, seed=3, device=str(dev), prefix="", arch="qwen3")
+    cpath = os.path.join(tempfile.gettempdir(), f"acb_bench_cond_q8_0_r{rank}.gguf")
+    synthetic.write_dit_gguf(cpath, dict(synthetic.ACESTEP_DIT_2B), synthetic.Q8_0, seed=21, device=str(dev),
+                             cond=dict(synthetic.ACESTEP_COND), decoder=False)
+    enc = acb.Qwen3Encoder(tpath, device=dev.index or 0)
+    cond = acb.CondEncoder(cpath, device=dev.index or 0)
+    os.remove(tpath)
+    os.remove(cpath)
+    rng = np.random.default_rng(42)
+    text_ids = rng.integers(0, tcfg["vocab_size"], 70).astype(np.int32)
+    lyric_ids = rng.integers(0, tcfg["vocab_size"], 167).astype(np.int32)
+    timbre = rng.standard_normal((1, synthetic.ACESTEP_COND["latent_dim"])).astype(np.float32)
+
+    def chain():
+        return cond.forward(enc.forward(text_ids), enc.embed_lookup(lyric_ids), timbre)
+
+    for _ in range(3):
+        out = chain()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        out = chain()
+        times.append((time.perf_counter() - t0) * 1e3)
+    enc.close()
+    cond.close()
+    ms = float(np.median(times))
+    return {
+        "metric": "conditioning ms (the reference's logged case: text encoder 70 tokens + lyric 167 -> enc_S 238)",
+        "value": round(ms, 3), "unit": "ms", "higher_is_better": False,
+        "config": {"workload": "cond_logged_case", "text_tokens": 70, "lyric_tokens": 167, "timbre_rows": 1,
+                   "enc_rows": int(out.shape[0]), "text_encoder": "Qwen3-0.6B shape, BF16",
+                   "cond_encoder": "lyric 8L + timbre 4L, Q8_0", "mode": "exact"},
+        "e2e": {"value": round(ms, 3), "unit": "ms",
+                "path": "acb_qwen3_forward + acb_qwen3_embed_lookup + acb_cond_forward (host buffers)",
+                "h2d_bytes_per_step": int(text_ids.nbytes + lyric_ids.nbytes + timbre.nbytes),
+                "d2h_bytes_per_step": int(out.nbytes)},
+        "reference_published": "15.9 ms warm on an RTX PRO 6000, ggml-CUDA (tests/CUDA0-Q8_0.log:433; "
+                               "other hardware, context only)",
+        "finite": bool(np.isfinite(out).all()),
+    }
 
 
 def vae_flops(vcfg, T) -> int:
@@ -1789,14 +1856,15 @@ def main():
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
     ap.add_argument("--lm5-gen", type=int, default=LM5_GEN, help="config 5 LM tokens (profiling runs use fewer)")
-    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,ditlog,lm5,dit5",
+    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,ditlog,condlog,lm5,dit5",
                     help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
                          "decode), enc (config 1 text encoder), vae (the audio decoder on 86.8 s), ditlog (the DiT "
-                         "generation the reference logs: 1 track, turbo, no CFG) -- those five at "
+                         "generation the reference logs: 1 track, turbo, no CFG), condlog (the conditioning it logs) -- "
+                         "those six at "
                          "N=1 as sub-results -- and lm5 "
                          "(config 5's 4B Q4_K_M LM, one sequence per GPU, at every N), dit5 (config 5's DiT leg, "
                          "track pairs per GPU, at every N); without dit, ops is the "
-                         "headline; or one of gemv / gemm / enc / vae / ditlog / ditmodes / lm5 alone")
+                         "headline; or one of gemv / gemm / enc / vae / ditlog / condlog / ditmodes / lm5 alone")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

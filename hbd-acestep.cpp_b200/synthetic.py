@@ -16,7 +16,7 @@ import numpy as np
 
 import acb
 
-Q8_0, Q4_K, Q6_K, F32 = acb.Q8_0, acb.Q4_K, acb.Q6_K, acb.F32
+Q8_0, Q4_K, Q6_K, F32, BF16 = acb.Q8_0, acb.Q4_K, acb.Q6_K, acb.F32, acb.BF16
 
 QWEN3_1_7B = dict(vocab_size=217472, hidden_size=2048, intermediate_size=6144, num_hidden_layers=28,
                   num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1000000.0,
@@ -31,6 +31,11 @@ QWEN3_4B = dict(vocab_size=217472, hidden_size=2560, intermediate_size=9728, num
 
 def policy_q8_0(name: str, layer: int, n_layers: int) -> int:
     return Q8_0
+
+
+def policy_bf16(name: str, layer: int, n_layers: int) -> int:
+    """Every matrix BF16, as convert.py stores an unquantised model (the reference's text encoder)."""
+    return BF16
 
 
 def policy_q4_k_m(name: str, layer: int, n_layers: int) -> int:
@@ -65,6 +70,8 @@ def lm_tensors(cfg: dict, policy=policy_q8_0, seed: int = 0, device: str = "cuda
     def mat(name, N, K, layer):
         qt = policy(name, layer, L)
         w = torch.randn((N, K), generator=g, device=device) * 0.02
+        if qt == BF16:  # bits of the round-to-nearest-even bf16 values, [N][2K] bytes
+            return name, qt, w.to(torch.bfloat16).view(torch.int16).cpu().numpy().view(np.uint8), K
         return name, qt, quantize_on_device(w, qt), K
 
     def gain(name, n):
