@@ -1,6 +1,8 @@
 // weights.cpp -- device weight arena (see weights.h).
 #include "weights.h"
 
+#include <algorithm>
+
 #include <cstring>
 
 #include "host_common.h"
@@ -49,6 +51,16 @@ DevTensor * WeightArena::try_load(const GGUFFile & gf, const std::string & name)
 DevTensor * WeightArena::get(const std::string & name) const {
     const auto it = by_name_.find(name);
     return it == by_name_.end() ? nullptr : it->second;
+}
+
+std::vector<std::string> WeightArena::names() const {
+    std::vector<std::string> out;
+    out.reserve(by_name_.size());
+    for (const auto & kv : by_name_) {
+        out.push_back(kv.first);
+    }
+    std::sort(out.begin(), out.end());
+    return out;
 }
 
 DevTensor * WeightArena::load(const GGUFFile & gf, const std::string & name) {

@@ -46,6 +46,8 @@ class WeightArena {
     DevTensor * add_host(int type, int64_t K, int64_t N, const void * src, size_t nbytes);
     // The tensor loaded under a GGUF name (load / try_load / load_f32), or nullptr.
     DevTensor * get(const std::string & name) const;
+    // names of the tensors loaded one by one (not the fused ones), sorted
+    std::vector<std::string> names() const;
 
     // wctx_alloc: one cudaMalloc and every pending upload.
     acb_status upload(cudaStream_t st);

@@ -159,6 +159,16 @@ ACB_API acb_status acb_quantize(const float * x, int64_t rows, int64_t K, int ty
  * rounded to f32 once, multiplied by scaling, rounded to bf16 and added. rank <= 1024. */
 ACB_API acb_status acb_lora_delta_add(float * w, int64_t N, int64_t K, const float * A, const float * B, int rank,
                                       float scaling, acb_stream_t stream);
+/* LyCORIS LoKr delta (src/adapter-merge.h:674-958 with the merge of :357-472) on f32 rows w [N][K]
+ * (the dequantised base), N = a*c, K = b*d: delta[i*c + k][j*d + l] = fl32(w1s[i][j] * w2[k][l])
+ * with w1s [a][b] = w1 * (alpha / rank) and w2 [c][d] (the factor product w2_a . w2_b, or w2) in
+ * f32, rounded to bf16. Without dora_scale: w += bf16(delta) * user_scale. With dora_scale [N]
+ * (weight decomposition): m = w + bf16(delta), w = m * s per row, s = dora_scale[n] / (|m| + 2^-7)
+ * and, for user_scale != 1, s = s * user_scale + (1 - user_scale); |m| from the row's f32 squares
+ * summed in double. */
+ACB_API acb_status acb_lokr_delta_add(float * w, int64_t N, int64_t K, const float * w1s, int a, int b,
+                                      const float * w2, int c, int d, float user_scale, const float * dora_scale,
+                                      acb_stream_t stream);
 /* f32 rows back into a GGUF type: Q8_0 / Q4_K / Q6_K (acb_quantize), BF16 / F16 (nearest even), F32
  * (copy). The requantisation step of the adapter merge. */
 ACB_API acb_status acb_requant(const float * x, int64_t rows, int64_t K, int type, void * dst, acb_stream_t stream);

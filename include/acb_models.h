@@ -236,8 +236,10 @@ ACB_API acb_status acb_dit_load(const char * gguf_path, int device, acb_dit ** o
  * merged into the decoder weights at load with user scale adapter_scale, before the resident
  * copies are built: base dequantised, + bf16(alpha/rank * scale * B.A), requantised to its GGUF
  * type on the device (Q8_0 with ggml's quantiser; Q4_K / Q6_K with this library's encoders, which
- * choose their scales differently from ggml's search). adapter_path NULL is acb_dit_load. A LoKr
- * payload returns ACB_ERR_UNSUPPORTED. */
+ * choose their scales differently from ggml's search). A LyCORIS LoKr file (lycoris_<path> modules,
+ * adapter_merge_lokr) merges base + bf16(kron(w1 * alpha/rank, W2)) * scale, or with a
+ * dora_scale vector the weight decomposition of acb_lokr_delta_add. adapter_path NULL is
+ * acb_dit_load; ACB_ERR_FORMAT when no pair or module matches a weight. */
 ACB_API acb_status acb_dit_load_ex(const char * gguf_path, int device, const char * adapter_path,
                                    float adapter_scale, acb_dit ** out);
 ACB_API acb_status acb_dit_get_config(const acb_dit * m, acb_dit_config * cfg);

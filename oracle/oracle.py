@@ -1027,6 +1027,57 @@ def lora_merge(entry, A, B, scaling):
     return qt, out, merged
 
 
+def lokr_factors(w1, alpha, rank, w2=None, w2a=None, w2b=None):
+    """adapter_merge_lokr's two Kronecker factors (src/adapter-merge.h:674-958): w1s = w1 * (alpha /
+    rank) in f32, and W2 = w2 (monolithic) or w2_a . w2_b (factorised) with the exact products of
+    the f32 factors summed in float64 in ascending rank and rounded to f32 once."""
+    f = np.float32
+    scaling = f(f(alpha) / f(rank))
+    w1s = (np.asarray(w1, np.float32) * scaling).astype(np.float32)
+    if w2 is not None:
+        W2 = np.asarray(w2, np.float32)
+    else:
+        a, b = np.asarray(w2a, np.float32), np.asarray(w2b, np.float32)
+        acc = np.zeros((a.shape[0], b.shape[1]), np.float64)
+        for q in range(a.shape[1]):
+            acc += a[:, q:q + 1].astype(np.float64) * b[q:q + 1, :].astype(np.float64)
+        W2 = acc.astype(np.float32)
+    return w1s, W2
+
+
+def lokr_merge(entry, w1s, W2, user_scale, dora_scale=None):
+    """One tensor of adapter_merge_lokr + adapter_merge_on_backend (:357-472): delta = kron(w1s, W2)
+    (f32 products) rounded to bf16; without DoRA base + delta * user_scale; with a DoRA magnitude
+    vector m = base + delta, each row scaled by ds / (|m| + 2^-7), mixed with 1 by user_scale when
+    it is not 1 (|m| from the f32 squares summed in float64, rounded once, f32 sqrt). Returns
+    (qtype, merged raw, merged f32) like lora_merge."""
+    f = np.float32
+    qt, raw, K, shape = entry
+    N = int(np.prod(shape)) // K
+    base = _f32_of(entry).reshape(N, K)
+    delta = round_bf16(np.kron(w1s.astype(np.float32), W2.astype(np.float32)).astype(np.float32))
+    assert delta.shape == (N, K)
+    if dora_scale is None:
+        merged = (base + (delta * f(user_scale)).astype(np.float32)).astype(np.float32)
+    else:
+        m = (base + delta).astype(np.float32)
+        ss = (m * m).astype(np.float32).astype(np.float64).sum(axis=1).astype(np.float32)
+        rn = (np.sqrt(ss).astype(np.float32) + f(0.0078125)).astype(np.float32)
+        sc = (np.asarray(dora_scale, np.float32).reshape(N) / rn).astype(np.float32)
+        if f(user_scale) != f(1.0):
+            sc = ((sc * f(user_scale)).astype(np.float32) + f(f(1.0) - f(user_scale))).astype(np.float32)
+        merged = (m * sc[:, None]).astype(np.float32)
+    if qt == F32:
+        out = merged
+    elif qt == BF16:
+        out = f32_to_bf16_bits(merged)
+    elif qt == F16:
+        out = merged.astype(np.float16).view(np.uint16)
+    else:
+        out = quantize(merged, qt)
+    return qt, out, merged
+
+
 # ---- VAE decoder (src/vae.h) ----------------------------------------------------------------------
 
 class OracleVAE:

@@ -7,9 +7,13 @@
   (diffusion_model.* keys, lora_down / lora_up, per-tensor alpha scalars) generates what the
   oracle generates from the merged tensors, at the DiT bars (cosine >= 0.9999, max_rel <= 1e-2),
   and differs from the unmerged model;
-- a LoKr payload is refused with ACB_ERR_UNSUPPORTED.
+- LyCORIS LoKr (adapter_merge_lokr): the Kronecker delta with factorised and monolithic second
+  factors and the DoRA weight decomposition, bit for bit at kernel level (acb_lokr_delta_add) and
+  at the DiT bars through acb_dit_load_ex with a lycoris_* file; a LoKr payload with no usable
+  module is refused with ACB_ERR_FORMAT.
 Safetensors files are written here by a small writer of the format (8-byte header length, JSON
 header, data)."""
+import ctypes as C
 import json
 import os
 import struct
@@ -169,10 +173,89 @@ def test_dit_comfyui_file_with_alpha_scalars(dit_file, tmp_path):
     _check_generate(path, f, 1.0, merged, keep)
 
 
-def test_lokr_refused(dit_file, tmp_path):
+def test_lokr_without_usable_module_refused(dit_file, tmp_path):
     path, _ = dit_file
     f = str(tmp_path / "lokr.safetensors")
+    # a LoKr marker but no lycoris_ module with w1, w2 and alpha: nothing merges
     write_safetensors(f, {"layers.0.self_attn.q_proj.lokr_w1": ("F32", np.ones((4, 4), np.float32))})
     with pytest.raises(acb.AcbError) as e:
         acb.DiT(path, adapter=f)
-    assert e.value.status == 2
+    assert e.value.status == 7
+
+
+@pytest.mark.parametrize("qt,form,dora,user", [(acb.Q8_0, "factor", False, 0.8), (acb.Q8_0, "mono", True, 0.8),
+                                               (acb.BF16, "factor", True, 1.0), (acb.BF16, "mono", False, 1.0)])
+def test_lokr_kernels_bitexact(cuda, qt, form, dora, user):
+    import torch
+    rng = np.random.default_rng(40 + qt + (form == "mono") + 2 * dora)
+    a, b, c, d, r = 4, 8, 96, 64, 8
+    N, K = a * c, b * d
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    raw = O.quantize(w, qt) if qt != acb.BF16 else _bf16(w)
+    entry = (qt, raw, K, (N, K))
+    w1 = (rng.standard_normal((a, b)) * 0.1).astype(np.float32)
+    if form == "factor":
+        w1s, W2 = O.lokr_factors(w1, 16.0, r, w2a=(rng.standard_normal((c, r)) * 0.1).astype(np.float32),
+                                 w2b=(rng.standard_normal((r, d)) * 0.1).astype(np.float32))
+    else:
+        w1s, W2 = O.lokr_factors(w1, 16.0, r, w2=(rng.standard_normal((c, d)) * 0.05).astype(np.float32))
+    ds = (1.0 + 0.1 * rng.standard_normal(N)).astype(np.float32) * np.float32(0.1) if dora else None
+    _, ref_raw, _ = O.lokr_merge(entry, w1s, W2, user, ds)
+    d_raw = torch.from_numpy(np.ascontiguousarray(raw).view(np.uint8).copy()).cuda()
+    ids = torch.arange(N, dtype=torch.int32, device="cuda")
+    tmp = torch.empty((N, K), dtype=torch.float32, device="cuda")
+    acb._check("acb_get_rows", acb.lib().acb_get_rows(d_raw.data_ptr(), qt, N, K, ids.data_ptr(), N, tmp.data_ptr(),
+                                                      acb.F32, K, None, acb._stream(None)))
+    d1, d2 = torch.from_numpy(w1s).cuda(), torch.from_numpy(W2).cuda()
+    dds = torch.from_numpy(ds).cuda() if dora else None
+    fn = acb.lib().acb_lokr_delta_add
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int,
+                   C.c_float, C.c_void_p, C.c_void_p]
+    acb._check("acb_lokr_delta_add", fn(tmp.data_ptr(), N, K, d1.data_ptr(), a, b, d2.data_ptr(), c, d, user,
+                                        dds.data_ptr() if dora else None, acb._stream(None)))
+    out = torch.empty_like(d_raw)
+    acb._check("acb_requant", acb.lib().acb_requant(tmp.data_ptr(), N, K, qt, out.data_ptr(), acb._stream(None)))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().reshape(-1), np.ascontiguousarray(ref_raw).view(np.uint8).reshape(-1))
+
+
+# (target, a, b, form): factorised modules of rank 4, monolithic ones of linear_dim 6
+LOKR = [("layers.0.self_attn.q_proj", 4, 4, "factor"), ("layers.0.self_attn.v_proj", 2, 4, "mono"),
+        ("layers.1.cross_attn.o_proj", 4, 8, "factor"), ("layers.1.mlp.down_proj", 2, 2, "mono")]
+
+
+def test_dit_lokr_file(dit_file, tmp_path):
+    path, keep = dit_file
+    rng = np.random.default_rng(13)
+    shapes = {t: (N, K) for t, N, K in TARGETS}
+    tens, merged, user, lin_dim = {}, dict(keep), 0.9, 6
+    for i, (t, a, b, form) in enumerate(LOKR):
+        N, K = shapes[t]
+        c, d = N // a, K // b
+        key = "lycoris_" + t.replace(".", "_")
+        w1 = (rng.standard_normal((a, b)) * 0.5).astype(np.float32)
+        alpha = float(3 + i)
+        tens[f"{key}.lokr_w1"] = ("F32", w1)
+        tens[f"{key}.alpha"] = ("F32", np.array(alpha, dtype=np.float32).reshape(()))
+        if form == "factor":
+            w2a = (rng.standard_normal((c, 4)) * 0.3).astype(np.float32)
+            w2b = (rng.standard_normal((4, d)) * 0.3).astype(np.float32)
+            tens[f"{key}.lokr_w2_a"] = ("F32", w2a)
+            tens[f"{key}.lokr_w2_b"] = ("BF16", _bf16(w2b))  # read as f32 without a second rounding
+            w1s, W2 = O.lokr_factors(w1, alpha, 4, w2a=w2a, w2b=O.round_bf16(w2b))
+        else:
+            w2 = (rng.standard_normal((c, d)) * 0.1).astype(np.float32)
+            tens[f"{key}.lokr_w2"] = ("F32", w2)
+            w1s, W2 = O.lokr_factors(w1, alpha, lin_dim, w2=w2)
+        ds = None
+        if i == 2:  # one module with a DoRA magnitude vector
+            ds = (np.abs(rng.standard_normal(N)) + 0.5).astype(np.float32)
+            tens[f"{key}.dora_scale"] = ("F32", ds.reshape(N, 1))
+        name = f"decoder.{t}.weight"
+        qt, raw, K_, shape = keep[name]
+        _, mraw, _ = O.lokr_merge((qt, raw, K_, shape), w1s, W2, user, ds)
+        merged[name] = (qt, np.ascontiguousarray(mraw).reshape(raw.shape), K_, shape)
+    f = str(tmp_path / "lokr.safetensors")
+    write_safetensors(f, tens, {"lokr_config": json.dumps({"linear_dim": lin_dim, "factor": -1})})
+    _check_generate(path, f, user, merged, keep)
