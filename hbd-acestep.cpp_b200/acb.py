@@ -1096,7 +1096,8 @@ class DiT:
 
     def generate_ex(self, noise, context, enc, schedule, guidance_scale=1.0, solver="euler", real_S=None,
                     real_enc_S=None, seeds=None, randn=None, cancel=None, context_switch=None, cover_steps=-1,
-                    enc_switch=None, real_enc_S_switch=None, dcw_scaler=0.0, stork_substeps=10):
+                    enc_switch=None, real_enc_S_switch=None, dcw_scaler=0.0, stork_substeps=10, dcw_high_scaler=0.0,
+                    dcw_mode="low"):
         """acb_dit_generate_ex (dit_ggml_generate's argument list). randn(seed, n) -> n floats is
         the SDE noise source; cancel(step_count) -> bool is polled before every step. Returns
         (x0, device ms); raises AcbError with status 9 when cancelled."""
@@ -1130,7 +1131,8 @@ class DiT:
             self.h, noise.ctypes.data, context.ctypes.data, enc.ctypes.data, enc.shape[1], T, N, sched.size,
             sched.ctypes.data, out.ctypes.data, float(guidance_scale), ptr(cs), int(cover_steps),
             C.cast(cb_c, C.c_void_p) if cb_c else None, None, ptr(rs), ptr(re), ptr(es), ptr(res), ptr(sd), 1,
-            float(dcw_scaler), 0.0, b"low", solver.encode() if solver else None, int(stork_substeps),
+            float(dcw_scaler), float(dcw_high_scaler), dcw_mode.encode() if dcw_mode else None,
+            solver.encode() if solver else None, int(stork_substeps),
             C.cast(cb_r, C.c_void_p) if cb_r else None, None, C.cast(C.pointer(ms), C.c_void_p)))
         return out, ms.value
 

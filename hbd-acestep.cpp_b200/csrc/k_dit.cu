@@ -191,6 +191,48 @@ __global__ void dit_sde_kernel(float * __restrict__ xt, const float * __restrict
 
 using namespace acb;
 
+// DCW (src/dit-sampler.h:613-666, src/dwt-haar.h) after an ODE solver step: denoised = xt - vt *
+// t_next; modes 0 low / 1 high / 2 double move the Haar bands of xt (frames 2j, 2j+1 along T,
+// zero-padded on odd T) away from the denoised sample's by s_low / s_high, then invert; mode 3
+// (pix) moves xt itself by s_low. One thread per (track, frame pair, channel) -- pix: per element.
+__global__ void dit_dcw_kernel(float * __restrict__ xt, const float * __restrict__ vt, int T, int C, int Tl,
+                               int64_t n_items, float t_next, int mode, float s_low, float s_high) {
+    const int64_t idx = (int64_t) blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_items) {
+        return;
+    }
+    if (mode == ACB_DCW_PIX) {
+        const float den = __fsub_rn(xt[idx], __fmul_rn(vt[idx], t_next));
+        xt[idx]         = __fadd_rn(xt[idx], __fmul_rn(s_low, __fsub_rn(xt[idx], den)));
+        return;
+    }
+    const float   r     = 0.70710678118654752440f;
+    const int64_t c     = idx % C;
+    const int64_t q     = idx / C;
+    const int64_t tl    = q % Tl;
+    const int64_t b     = q / Tl;
+    const int64_t i0    = ((b * T) + 2 * tl) * C + c;
+    const bool    has_b = 2 * tl + 1 < T;
+    const int64_t i1    = i0 + C;
+    const float   xa = xt[i0], xb = has_b ? xt[i1] : 0.0f;
+    const float   da = __fsub_rn(xa, __fmul_rn(vt[i0], t_next));
+    const float   db = has_b ? __fsub_rn(xb, __fmul_rn(vt[i1], t_next)) : 0.0f;
+    float xL = has_b ? __fmul_rn(__fadd_rn(xa, xb), r) : __fmul_rn(xa, r);
+    float xH = has_b ? __fmul_rn(__fsub_rn(xa, xb), r) : __fmul_rn(xa, r);
+    const float yL = has_b ? __fmul_rn(__fadd_rn(da, db), r) : __fmul_rn(da, r);
+    const float yH = has_b ? __fmul_rn(__fsub_rn(da, db), r) : __fmul_rn(da, r);
+    if (mode != ACB_DCW_HIGH && s_low != 0.0f) {
+        xL = __fadd_rn(xL, __fmul_rn(s_low, __fsub_rn(xL, yL)));
+    }
+    if (mode != ACB_DCW_LOW && s_high != 0.0f) {
+        xH = __fadd_rn(xH, __fmul_rn(s_high, __fsub_rn(xH, yH)));
+    }
+    xt[i0] = __fmul_rn(__fadd_rn(xL, xH), r);
+    if (has_b) {
+        xt[i1] = __fmul_rn(__fsub_rn(xL, xH), r);
+    }
+}
+
 static unsigned blocks_for(int64_t n, int threads) {
     return (unsigned) ((n + threads - 1) / threads);
 }
@@ -257,6 +299,18 @@ extern "C" acb_status acb_dit_euler(float * xt, const float * vt, const float * 
         return ACB_OK;
     }
     dit_euler_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(xt, vt, tt, last, out, n);
+    return launch_status();
+}
+
+extern "C" acb_status acb_dit_dcw(float * xt, const float * vt, int n_tracks, int T, int C, float t_next, int mode,
+                                  float s_low, float s_high, acb_stream_t stream) {
+    if (!xt || !vt || n_tracks <= 0 || T <= 0 || C <= 0 || mode < ACB_DCW_LOW || mode > ACB_DCW_PIX) {
+        return ACB_ERR_INVALID_ARG;
+    }
+    const int     Tl = (T + 1) / 2;
+    const int64_t n  = mode == ACB_DCW_PIX ? (int64_t) n_tracks * T * C : (int64_t) n_tracks * Tl * C;
+    dit_dcw_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t) stream>>>(xt, vt, T, C, Tl, n, t_next, mode, s_low,
+                                                                          s_high);
     return launch_status();
 }
 

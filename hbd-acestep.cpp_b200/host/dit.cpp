@@ -902,6 +902,8 @@ struct GenArgs {
     const int64_t * seeds             = nullptr;
     int             solver            = ACB_SOLVER_EULER;
     int             stork_substeps    = 10;
+    int             dcw_mode          = -1;  // ACB_DCW_* or -1: no DCW
+    float           dcw_scaler = 0.0f, dcw_high_scaler = 0.0f;
     acb_randn_fn    randn             = nullptr;
     void *          randn_data        = nullptr;
     float *         gpu_ms            = nullptr;
@@ -1218,6 +1220,20 @@ acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * ho
         const float * v = do_cfg ? m->vt.as<float>() : m->vel.as<float>();
         ACB_TRY(acb_stork4_step(stork, m->xt.as<float>(), v, t_curr, t_next, (acb_stream_t) s));
     }
+    if (g.dcw_mode >= 0 && !last && !sde) {
+        // DCW after the solver step (dit-sampler.h:613-666) with this step's effective scales; a
+        // zero scale leaves xt as it is (the reference returns before its transform)
+        const int   md = g.dcw_mode;
+        const float hi = md == ACB_DCW_DOUBLE ? g.dcw_high_scaler : g.dcw_scaler;
+        const float sl = md == ACB_DCW_PIX ? g.dcw_scaler : t_curr * g.dcw_scaler;
+        const float sh = (1.0f - t_curr) * hi;
+        const bool  run = md == ACB_DCW_HIGH ? sh != 0.0f : md == ACB_DCW_DOUBLE ? (sl != 0.0f || sh != 0.0f)
+                                                                                 : sl != 0.0f;
+        if (run) {
+            const float * v = do_cfg ? m->vt.as<float>() : m->vel.as<float>();
+            ACB_TRY(acb_dit_dcw(m->xt.as<float>(), v, n, T, Oc, t_next, md, sl, sh, (acb_stream_t) s));
+        }
+    }
     if (host_out && cudaMemcpyAsync(host_out, last ? m->out.p : m->xt.p, n_tot * 4, cudaMemcpyDeviceToHost, s) !=
                         cudaSuccess) {
         return ACB_ERR_CUDA;
@@ -1357,11 +1373,6 @@ extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, cons
                                           float dcw_high_scaler, const char * dcw_mode, const char * solver_name,
                                           int stork_substeps, acb_randn_fn randn, void * randn_data, float * gpu_ms) {
     (void) use_batch_cfg;   // both settings run the batched graph: HBM is not the constraint here
-    (void) dcw_mode;
-    if (dcw_scaler > 0.0f || dcw_high_scaler > 0.0f) {
-        set_last_error("acb_dit_generate_ex: DCW (dwt-haar.h) is not provided by this library");
-        return ACB_ERR_UNSUPPORTED;
-    }
     int solver = ACB_SOLVER_EULER;  // solver_lookup: NULL or "" is euler; an unknown name falls back to it
     if (solver_name && std::strcmp(solver_name, "dpm3m") == 0) {
         solver = ACB_SOLVER_DPM3M;
@@ -1395,6 +1406,18 @@ extern "C" acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, cons
     g.randn             = randn;
     g.randn_data        = randn_data;
     g.gpu_ms            = gpu_ms;
+    if (dcw_scaler > 0.0f || dcw_high_scaler > 0.0f) {  // the mode names of dit-sampler.h:632-640
+        g.dcw_mode        = ACB_DCW_LOW;  // also an unknown or missing name
+        g.dcw_scaler      = dcw_scaler;
+        g.dcw_high_scaler = dcw_high_scaler;
+        if (dcw_mode && std::strcmp(dcw_mode, "high") == 0) {
+            g.dcw_mode = ACB_DCW_HIGH;
+        } else if (dcw_mode && std::strcmp(dcw_mode, "double") == 0) {
+            g.dcw_mode = ACB_DCW_DOUBLE;
+        } else if (dcw_mode && std::strcmp(dcw_mode, "pix") == 0) {
+            g.dcw_mode = ACB_DCW_PIX;
+        }
+    }
     return generate_impl(m, g);
 }
 

@@ -402,6 +402,18 @@ ACB_API acb_status acb_dit_apg(const float * cond, const float * uncond, double 
  * out = xt - vt * t_curr (the x0 prediction, dit-sampler.h:596-604). */
 ACB_API acb_status acb_dit_euler(float * xt, const float * vt, const float * tt, int last, float * out, int64_t n,
                                  acb_stream_t stream);
+/* DCW, Differential Correction in the Wavelet domain (src/dit-sampler.h:613-666, src/dwt-haar.h),
+ * in place on xt [n_tracks][T][C] right after an ODE solver step (not after the last step, not
+ * for SDE): denoised = xt - vt * t_next; for the wavelet modes the orthonormal Haar transform of
+ * frame pairs (2j, 2j+1) along T (zero padding on odd T), the low band moved by s_low * (xL - yL)
+ * (ACB_DCW_LOW, DOUBLE) and the high band by s_high * (xH - yH) (HIGH, DOUBLE), then the inverse;
+ * ACB_DCW_PIX: xt += s_low * (xt - denoised). Every op one f32 rounding. The caller passes the
+ * step's effective scales (low: t_curr * dcw_scaler; high: (1 - t_curr) * dcw_scaler; double:
+ * those two with dcw_high_scaler for the high band; pix: dcw_scaler) and skips the call when they
+ * are zero, as the reference returns before its transform. */
+enum { ACB_DCW_LOW = 0, ACB_DCW_HIGH = 1, ACB_DCW_DOUBLE = 2, ACB_DCW_PIX = 3 };
+ACB_API acb_status acb_dit_dcw(float * xt, const float * vt, int n_tracks, int T, int C, float t_next, int mode,
+                               float s_low, float s_high, acb_stream_t stream);
 /* DPM++ 3M step, the "dpm3m" solver (src/solvers/solver-dpm.h:14-50; registry solver-registry.h:32):
  * tt = {t_curr, t_r, t_next}, dt = t_curr - t_next; history = velocities stored so far, capped at 2
  * (the step index for steps 0, 1, then 2). history 0: xt -= vt*dt; 1: xt -= (1.5 vt - 0.5 prev)*dt;

@@ -345,9 +345,11 @@ typedef void (*acb_randn_fn)(int64_t seed, float * out, int n, void * data);
  *   real_S[N] / real_enc_S[N]: padding masks (:244-304; NULL: no padding);
  *   seeds[N] + randn / randn_data: the SDE solver's per-step noise (seed_b + step + 1);
  *   use_batch_cfg: accepted, both values run the batched graph (results equal up to summation order);
- *   dcw_*: DCW is not provided (dcw_scaler or dcw_high_scaler > 0: ACB_ERR_UNSUPPORTED);
- *   solver_name: "euler" (also NULL / ""), "dpm3m", "sde"; "stork4": ACB_ERR_UNSUPPORTED; any
- *   other name falls back to Euler, as solver_lookup's caller does;
+ *   dcw_scaler / dcw_high_scaler / dcw_mode: DCW after every ODE step but the last (either scaler
+ *   > 0; modes "low" (also NULL or unknown), "high", "double", "pix"; acb_dit_dcw), not with SDE;
+ *   solver_name: "euler" (also NULL / ""), "dpm3m", "sde", "stork4" (after
+ *   acb_dit_set_stork4_tables; before it ACB_ERR_UNSUPPORTED); any other name falls back to Euler,
+ *   as solver_lookup's caller does;
  *   gpu_ms (optional): device time of the step loop.
  * Returns ACB_OK where the reference returns 0. */
 ACB_API acb_status acb_dit_generate_ex(acb_dit * m, const float * noise, const float * context_latents,

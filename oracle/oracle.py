@@ -598,7 +598,8 @@ def dit_from_gguf_tensors(cfg, tensors):
 
 def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, momentum=-0.75, norm_threshold=2.5,
                  solver="euler", real_S=None, real_enc_S=None, seeds=None, randn=None, context_switch=None,
-                 cover_steps=-1, enc_switch=None, real_enc_S_switch=None, stork_tables=None, stork_substeps=10):
+                 cover_steps=-1, enc_switch=None, real_enc_S_switch=None, stork_tables=None, stork_substeps=10,
+                 dcw_scaler=0.0, dcw_high_scaler=0.0, dcw_mode="low"):
     """dit_ggml_generate (src/dit-sampler.h:132-711) over an OracleDiT with the Euler solver,
     DPM++ 3M (solver="dpm3m", solver-dpm.h:14-50) or SDE ancestral (solver="sde",
     solver-sde.h:17-38; randn(seed, n) gives the fresh noise of track b at step k from seed
@@ -655,18 +656,73 @@ def dit_generate(od, noise, context, enc, null_emb, schedule, guidance_scale, mo
             return (xt - v * np.float32(t)).astype(np.float32)
         if solver == "dpm3m":
             xt, hist1, hist2 = dpm3m_step(xt, v, hist1, hist2, t, schedule[step + 1])
-            continue
-        if stork is not None:
+        elif stork is not None:
             xt = stork.step(xt, v, t, schedule[step + 1])
-            continue
-        if solver == "sde":
+        elif solver == "sde":
             fresh = np.stack([np.asarray(randn(int(seeds[b]) + step + 1, T * Oc), np.float32).reshape(T, Oc)
                               for b in range(N)])
             xt = sde_step(xt, v, fresh, t, schedule[step + 1])
-            continue
-        dt = np.float32(np.float32(t) - np.float32(schedule[step + 1]))
-        xt = (xt - v * dt).astype(np.float32)
+            continue  # SDE injects noise: no DCW
+        else:
+            dt = np.float32(np.float32(t) - np.float32(schedule[step + 1]))
+            xt = (xt - v * dt).astype(np.float32)
+        if dcw_scaler > 0.0 or dcw_high_scaler > 0.0:
+            xt = dcw_step(xt, v, t, schedule[step + 1], dcw_scaler, dcw_high_scaler, dcw_mode)
     return xt
+
+
+def _haar_fwd(x):
+    """dwt_haar_fwd_tc (src/dwt-haar.h:24-50) along axis 1 of [N][T][C] f32 (zero-padded odd T)."""
+    f, r = np.float32, np.float32(0.70710678118654752440)
+    N, T, C = x.shape
+    a = x[:, 0::2]
+    b = np.zeros_like(a)
+    b[:, :x[:, 1::2].shape[1]] = x[:, 1::2]
+    L = ((a + b).astype(f) * r).astype(f)
+    H = ((a - b).astype(f) * r).astype(f)
+    if T % 2:  # the lone last frame: L = H = a / sqrt(2)
+        L[:, -1] = (a[:, -1] * r).astype(f)
+        H[:, -1] = (a[:, -1] * r).astype(f)
+    return L, H
+
+
+def _haar_inv(L, H, T):
+    """dwt_haar_inv_tc (:54-75): exactly T frames."""
+    f, r = np.float32, np.float32(0.70710678118654752440)
+    out = np.empty((L.shape[0], T, L.shape[2]), np.float32)
+    out[:, 0::2] = ((L + H).astype(f) * r).astype(f)
+    out[:, 1::2] = (((L - H).astype(f) * r).astype(f))[:, :T // 2]
+    return out
+
+
+def dcw_step(xt, v, t_curr, t_next, dcw_scaler, dcw_high_scaler, mode):
+    """DCW after an ODE solver step (src/dit-sampler.h:613-666, src/dwt-haar.h): denoised = xt -
+    v * t_next from the updated xt; modes low (s = t_curr * scaler on the low band), high ((1 -
+    t_curr) * scaler, high band), double (both, the high one with dcw_high_scaler), pix (xt +=
+    scaler * (xt - denoised), no transform); an unknown mode is low. A zero effective scale leaves
+    xt untouched (the reference returns before the transform)."""
+    f = np.float32
+    t_curr, t_next = f(t_curr), f(t_next)
+    mode = mode if mode in ("low", "high", "double", "pix") else "low"
+    s_low = f(t_curr * f(dcw_scaler))
+    s_high = f((f(1.0) - t_curr) * f(dcw_scaler))
+    s_dh = f((f(1.0) - t_curr) * f(dcw_high_scaler))
+    den = (xt - (v * t_next).astype(f)).astype(f)
+    if mode == "pix":
+        s = f(dcw_scaler)
+        return xt if s == 0 else (xt + (s * (xt - den).astype(f)).astype(f)).astype(f)
+    if (mode == "low" and s_low == 0) or (mode == "high" and s_high == 0) or \
+            (mode == "double" and s_low == 0 and s_dh == 0):
+        return xt
+    xL, xH = _haar_fwd(xt)
+    yL, yH = _haar_fwd(den)
+    if mode in ("low", "double") and s_low != 0:
+        xL = (xL + (s_low * (xL - yL).astype(f)).astype(f)).astype(f)
+    if mode == "high":
+        xH = (xH + (s_high * (xH - yH).astype(f)).astype(f)).astype(f)
+    if mode == "double" and s_dh != 0:
+        xH = (xH + (s_dh * (xH - yH).astype(f)).astype(f)).astype(f)
+    return _haar_inv(xL, xH, xt.shape[1])
 
 
 def dpm3m_step(xt, vt, prev_vt, prev_prev_vt, t_curr, t_next):

@@ -180,7 +180,7 @@ def test_dit_generate_ex_matches_oracle(cuda, tmp_path):
 
 def test_dit_generate_ex_cancel_and_unsupported(cuda, tmp_path):
     """The cancel callback is polled before every step; a cancelled run returns ACB_ERR_CANCELLED
-    and the model stays usable. STORK4 and DCW are reported as unsupported, nothing runs."""
+    and the model stays usable. STORK4 without its tables is reported as unsupported, nothing runs."""
     cfg = DIT_TINY
     path, keep = _model(tmp_path, cfg, seed=16)
     dit = acb.DiT(path)
@@ -197,10 +197,45 @@ def test_dit_generate_ex_cancel_and_unsupported(cuda, tmp_path):
     a, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, cancel=lambda k: False)
     b, _ = dit.generate(noise, ctx, enc, sched, guidance_scale=3.0)
     assert np.array_equal(a, b)
-    for kw in (dict(solver="stork4"), dict(dcw_scaler=0.5)):
-        with pytest.raises(acb.AcbError) as e:
-            dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, **kw)
-        assert e.value.status == 2
+    with pytest.raises(acb.AcbError) as e:
+        dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver="stork4")
+    assert e.value.status == 2
+    dit.close()
+
+
+def test_dit_generate_dcw_matches_oracle(cuda, tmp_path):
+    """DCW (dit-sampler.h:613-666, dwt-haar.h) through acb_dit_generate_ex: the four modes after
+    Euler steps, low after DPM++ 3M steps, all against the oracle's generate; DCW changes the
+    result, and with the SDE solver it is not applied. (Frame counts are multiples of the patch
+    size, so the transform's odd-T padding is pinned on the CPU, tests/test_solver_cpu.py.)"""
+    cfg = DIT_TINY
+    path, keep = _model(tmp_path, cfg, seed=18)
+    dit = acb.DiT(path)
+    od = O.dit_from_gguf_tensors(cfg, keep)
+    null = keep["null_condition_emb"][1].astype(np.float32)
+    rng = np.random.default_rng(19)
+    N, T, enc_S, Oc = 2, 78, 12, cfg["out_channels"]  # 39 tokens: frame pairs of the transform = tokens
+    noise = rng.standard_normal((N, T, Oc)).astype(np.float32)
+    ctx = rng.standard_normal((N, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    sched = acb.turbo_schedule(4)
+    plain, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0)
+    cases = [("euler", "low", 0.3, 0.0), ("euler", "high", 0.3, 0.0), ("euler", "double", 0.3, 0.2),
+             ("euler", "pix", 0.1, 0.0), ("dpm3m", "low", 0.3, 0.0)]
+    for solver, mode, sc, hs in cases:
+        x0, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver=solver, dcw_scaler=sc,
+                                dcw_high_scaler=hs, dcw_mode=mode)
+        ref = O.dit_generate(od, noise, ctx, enc, null, sched, 3.0, solver=solver, dcw_scaler=sc,
+                             dcw_high_scaler=hs, dcw_mode=mode)
+        assert np.isfinite(x0).all()
+        _check(x0, ref, 0.9999, 1e-2, f"dcw {solver} {mode}")
+        if solver == "euler":
+            assert max_rel(x0, plain) > 1e-3, mode  # the correction is applied
+    seeds = [5, 6]
+    a, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver="sde", seeds=seeds, randn=_np_randn,
+                           dcw_scaler=0.3)
+    b, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver="sde", seeds=seeds, randn=_np_randn)
+    assert np.array_equal(a, b)
     dit.close()
 
 

@@ -2,8 +2,10 @@
 restate its formula: the Adams-Bashforth weights of each order sum to one (a constant velocity
 field moves xt exactly like Euler), third order integrates a velocity that is quadratic in t
 exactly over uniform steps, second order a linear one, and the history moves down one slot per
-step with the reference's bootstrap (Euler, then second, then third order)."""
+step with the reference's bootstrap (Euler, then second, then third order). Also the oracle's DCW
+step against a frame-by-frame restatement of the Haar pair (odd T included)."""
 import numpy as np
+import pytest
 
 import oracle as O
 
@@ -65,3 +67,52 @@ def test_sde_step_endpoints():
     x0 = (x - (v * np.float32(0.7)).astype(np.float32)).astype(np.float32)
     assert np.array_equal(O.sde_step(x, v, z, 0.7, 0.0), x0)
     assert np.array_equal(O.sde_step(x, v, z, 0.7, 1.0), z)
+
+
+@pytest.mark.parametrize("T", [6, 7])
+def test_dcw_matches_loop_restatement(T):
+    """The oracle's DCW (dit-sampler.h:613-666 with dwt-haar.h) against a frame-by-frame restatement
+    of the Haar pair, including odd T (the last frame paired with zero and dropped on the way back)
+    and the zero-scale early return."""
+    f, r = np.float32, np.float32(0.70710678118654752440)
+    rng = np.random.default_rng(T)
+    xt = rng.standard_normal((2, T, 3)).astype(np.float32)
+    v = rng.standard_normal((2, T, 3)).astype(np.float32)
+    t_curr, t_next, sc, hs = 0.8, 0.6, 0.3, 0.2
+
+    def fwd(x):
+        Tl = (T + 1) // 2
+        L = np.zeros((x.shape[0], Tl, x.shape[2]), np.float32)
+        H = np.zeros_like(L)
+        for j in range(Tl):
+            a = x[:, 2 * j]
+            if 2 * j + 1 < T:
+                b = x[:, 2 * j + 1]
+                L[:, j], H[:, j] = ((a + b) * r).astype(f), ((a - b) * r).astype(f)
+            else:
+                L[:, j], H[:, j] = (a * r).astype(f), (a * r).astype(f)
+        return L, H
+
+    def inv(L, H):
+        out = np.zeros((L.shape[0], T, L.shape[2]), np.float32)
+        for j in range(L.shape[1]):
+            out[:, 2 * j] = ((L[:, j] + H[:, j]) * r).astype(f)
+            if 2 * j + 1 < T:
+                out[:, 2 * j + 1] = ((L[:, j] - H[:, j]) * r).astype(f)
+        return out
+
+    den = (xt - (v * f(t_next)).astype(f)).astype(f)
+    xL, xH = fwd(xt)
+    yL, yH = fwd(den)
+    sl, sh, sdh = f(f(t_curr) * f(sc)), f((f(1) - f(t_curr)) * f(sc)), f((f(1) - f(t_curr)) * f(hs))
+    want = {
+        "low": inv((xL + (sl * (xL - yL)).astype(f)).astype(f), xH),
+        "high": inv(xL, (xH + (sh * (xH - yH)).astype(f)).astype(f)),
+        "double": inv((xL + (sl * (xL - yL)).astype(f)).astype(f), (xH + (sdh * (xH - yH)).astype(f)).astype(f)),
+        "pix": (xt + (f(sc) * (xt - den).astype(f)).astype(f)).astype(f),
+    }
+    for mode, ref in want.items():
+        got = O.dcw_step(xt, v, t_curr, t_next, sc, hs, mode)
+        assert np.array_equal(got, ref), mode
+    assert np.array_equal(O.dcw_step(xt, v, t_curr, t_next, sc, hs, "nonsense"), want["low"])
+    assert O.dcw_step(xt, v, 1.0, t_next, sc, 0.0, "high") is xt  # (1 - t_curr) * scaler = 0: untouched
