@@ -1577,7 +1577,7 @@ def run_dit_job(args, dev, rank, ws, local, stream):
                                   "traffic": None, "tensor_work_multiplier": 3 if mode == "exact" else 1}}
     dom = dominant_gemm(dev, n_loc * S, 2 * cfg["intermediate_size"], cfg["hidden_size"], peaks, kind)
     ex = out["exact"]
-    launches = dit.eval_kernels() + 2  # evaluation graph + APG + Euler per step
+    launches = dit.step_kernels()  # the step graph(s) of the last timed step: evaluation, APG, Euler
     line = {"metric": "DiT denoise steps/s (config 4: 24 layers, hidden 2048, Q8_0, 4 tracks x CFG 2 = 8 "
                       "sequences of 750 tokens, 512 condition rows, turbo Euler + APG)",
             "value": ex["value"], "unit": "step/s", "n_gpus": ws, "steps": ex["steps"], "warmup": max(args.warmup, 3),

@@ -129,6 +129,7 @@ def lib():
                                 P]),
             "acb_attn_vt": (I, [P, I, I64, I64, I, I, I, I, P, I64, I64, P]),
             "acb_dit_eval_kernels": (I, [P]),
+            "acb_dit_step_kernels": (I, [P]),
             "acb_dit_eval": (I, [P, P, P, P, P]),
             "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
             "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
@@ -1069,6 +1070,10 @@ class DiT:
         _check("acb_dit_forward", lib().acb_dit_forward(self.h, _ptr(x), _ptr(enc), N, T, enc.shape[1], float(t),
                                                         float(t_r), _ptr(out), n_layers_run, _stream(stream)))
         return out
+
+    def step_kernels(self) -> int:
+        """This library's kernel launches in the last denoise step of the generate / job drivers."""
+        return lib().acb_dit_step_kernels(self.h)
 
     def eval_kernels(self) -> int:
         """Kernel launches in the last captured evaluation graph."""

@@ -93,6 +93,8 @@ struct acb_dit {
     std::vector<int>                stork_ms;
     std::vector<double>             stork_fpa, stork_fpb, stork_recf;
     std::map<std::tuple<int, int, int, int, int, uint32_t>, cudaGraphExec_t> graphs;
+    std::map<std::tuple<int, int, int, int, int, uint32_t>, int> graph_kernels;  // kernel nodes per graph
+    int step_kernels = 0;  // kernel launches of the last denoise step run (its step graph(s))
 
     ~acb_dit();
 
@@ -885,6 +887,26 @@ extern "C" acb_status acb_dit_eval(acb_dit * m, const float * d_input, const flo
 
 namespace {
 
+// kernel nodes of a captured graph (every one is a launch of this library's kernels)
+int kernel_nodes(cudaGraph_t g) {
+    size_t n = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || n == 0) {
+        return 0;
+    }
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) {
+        return 0;
+    }
+    int k = 0;
+    for (cudaGraphNode_t nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) {
+            k++;
+        }
+    }
+    return k;
+}
+
 // The arguments of dit_ggml_generate (src/dit-sampler.h:132-158) that this library implements.
 struct GenArgs {
     const float *   noise = nullptr, *context = nullptr, *enc = nullptr;
@@ -934,6 +956,7 @@ struct DiTRun {
     cudaEvent_t  e0 = nullptr, e1 = nullptr, done[2] = { nullptr, nullptr };
     int          steps_run = 0;
     acb_stork4 * stork     = nullptr;  // the STORK4 state of this run (solver stork4)
+    int          last_kernels = 0;     // kernel nodes of the graph get_graph returned last
 
     ~DiTRun() {
         for (cudaEvent_t e : { e0, e1, done[0], done[1] }) {
@@ -1090,6 +1113,7 @@ acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphE
     auto       it    = m->graphs.find(key);
     if (it != m->graphs.end()) {
         *ex = it->second;
+        last_kernels = m->graph_kernels[key];
         return ACB_OK;
     }
     cudaGraph_t gr = nullptr;
@@ -1135,12 +1159,15 @@ acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphE
         set_last_error("DiT step graph capture failed");
         return st != ACB_OK ? st : ACB_ERR_CUDA;
     }
+    const int         nk = kernel_nodes(gr);
     const cudaError_t ie = cudaGraphInstantiate(ex, gr, 0);
     cudaGraphDestroy(gr);
     if (ie != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
     m->graphs.emplace(key, *ex);
+    m->graph_kernels[key] = nk;
+    last_kernels          = nk;
     return ACB_OK;
 }
 
@@ -1193,9 +1220,11 @@ acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * ho
     if (cudaMemcpyAsync(m->tt.p, tv.data(), 3 * sizeof(float), cudaMemcpyHostToDevice, s) != cudaSuccess) {
         return ACB_ERR_CUDA;
     }
+    int launched = 0;  // this library's kernels in this step
     if (half < 0) {
         cudaGraphExec_t ex = nullptr;
         ACB_TRY(get_graph(first, lst, hist, 0, &ex));
+        launched = last_kernels;
         if (cudaGraphLaunch(ex, s) != cudaSuccess) {
             return ACB_ERR_CUDA;
         }
@@ -1204,7 +1233,9 @@ acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * ho
         // [cond, uncond] pair (both ranks of the pair hold the same xt and take the same step)
         cudaGraphExec_t ea = nullptr, eb = nullptr;
         ACB_TRY(get_graph(first, lst, hist, 1, &ea));
+        launched = last_kernels;
         ACB_TRY(get_graph(first, lst, hist, 2, &eb));
+        launched += last_kernels;
         float * mine  = m->vpair.as<float>() + (size_t) half * n_per;
         float * other = m->vpair.as<float>() + (size_t) (1 - half) * n_per;
         if (cudaGraphLaunch(ea, s) != cudaSuccess ||
@@ -1232,8 +1263,10 @@ acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * ho
         if (run) {
             const float * v = do_cfg ? m->vt.as<float>() : m->vel.as<float>();
             ACB_TRY(acb_dit_dcw(m->xt.as<float>(), v, n, T, Oc, t_next, md, sl, sh, (acb_stream_t) s));
+            launched++;
         }
     }
+    m->step_kernels = launched;
     if (host_out && cudaMemcpyAsync(host_out, last ? m->out.p : m->xt.p, n_tot * 4, cudaMemcpyDeviceToHost, s) !=
                         cudaSuccess) {
         return ACB_ERR_CUDA;
@@ -1576,6 +1609,10 @@ extern "C" acb_status acb_dit_generate_sharded(acb_dit * m, acb_comm * comm, con
 
 extern "C" int acb_dit_eval_kernels(const acb_dit * m) {
     return m ? m->eval_kernels : 0;
+}
+
+extern "C" int acb_dit_step_kernels(const acb_dit * m) {
+    return m ? m->step_kernels : 0;
 }
 
 extern "C" void acb_dit_free(acb_dit * m) {

@@ -272,6 +272,11 @@ ACB_API acb_status acb_dit_eval(acb_dit * m, const float * d_input, const float 
                                 acb_stream_t stream);
 /* Kernel launches in the last captured evaluation graph (0 before the first acb_dit_eval). */
 ACB_API int        acb_dit_eval_kernels(const acb_dit * m);
+/* Kernel launches of this library in the last denoise step run by the generate / job drivers:
+ * the nodes of its step graph(s) (evaluation, guidance, solver) plus a DCW launch; the STORK4
+ * step's adaptive launches and the NCCL exchange are not counted. 0 before the first step. No
+ * reference counterpart: an accounting query. */
+ACB_API int        acb_dit_step_kernels(const acb_dit * m);
 
 /* dit_ggml_generate (dit-sampler.h:132-711) with the Euler solver, host arrays as in the reference:
  * noise [N][T][out_channels], context_latents [N][T][in_channels - out_channels], enc_hidden
