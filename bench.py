@@ -1110,6 +1110,7 @@ def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
     ms = e0.elapsed_time(e1) / reps
+    n_kernels = enc.forward_kernels()  # nodes of the forward's captured graph
     fl = enc_flops(cfg, S)
     # e2e: host ids in, host hidden states out (acb_qwen3_forward, the qwen3_forward drop-in)
     out = enc.forward(ids)
@@ -1133,7 +1134,7 @@ def run_enc(dev, rank, want_cpu=True, S=ENC_S, reps=50):
                      "flops_per_forward": fl, "traffic": None},
         "e2e": {"value": round(1.0 / e2e_s, 2), "unit": "forward/s", "h2d_bytes_per_step": S * 4,
                 "d2h_bytes_per_step": S * cfg["hidden_size"] * 4, "path": "acb_qwen3_forward"},
-        "gpu_launches_per_forward": 2 + cfg["num_hidden_layers"] * 12,
+        "gpu_launches_per_forward": n_kernels,
     }
     if want_cpu:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))

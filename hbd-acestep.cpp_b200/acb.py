@@ -130,6 +130,7 @@ def lib():
             "acb_attn_vt": (I, [P, I, I64, I64, I, I, I, I, P, I64, I64, P]),
             "acb_dit_eval_kernels": (I, [P]),
             "acb_dit_step_kernels": (I, [P]),
+            "acb_qwen3_forward_kernels": (I, [P]),
             "acb_dit_eval": (I, [P, P, P, P, P]),
             "acb_dit_apg": (I, [P, P, P, I, F, F, F, I, I, I, P, P]),
             "acb_dit_euler": (I, [P, P, P, I, P, I64, P]),
@@ -651,6 +652,10 @@ class Qwen3Encoder:
             self.h, _ptr(hidden), hidden.shape[0], layer_begin, layer_end, int(final_norm), _ptr(out),
             _stream(stream)))
         return out
+
+    def forward_kernels(self) -> int:
+        """This library's kernel launches in the last forward (the captured graph's nodes)."""
+        return lib().acb_qwen3_forward_kernels(self.h)
 
     def embed_lookup(self, ids):
         ids = self.np.ascontiguousarray(ids, dtype=self.np.int32)

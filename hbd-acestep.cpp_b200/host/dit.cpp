@@ -887,26 +887,6 @@ extern "C" acb_status acb_dit_eval(acb_dit * m, const float * d_input, const flo
 
 namespace {
 
-// kernel nodes of a captured graph (every one is a launch of this library's kernels)
-int kernel_nodes(cudaGraph_t g) {
-    size_t n = 0;
-    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || n == 0) {
-        return 0;
-    }
-    std::vector<cudaGraphNode_t> nodes(n);
-    if (cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) {
-        return 0;
-    }
-    int k = 0;
-    for (cudaGraphNode_t nd : nodes) {
-        cudaGraphNodeType t;
-        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) {
-            k++;
-        }
-    }
-    return k;
-}
-
 // The arguments of dit_ggml_generate (src/dit-sampler.h:132-158) that this library implements.
 struct GenArgs {
     const float *   noise = nullptr, *context = nullptr, *enc = nullptr;
@@ -1159,7 +1139,7 @@ acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphE
         set_last_error("DiT step graph capture failed");
         return st != ACB_OK ? st : ACB_ERR_CUDA;
     }
-    const int         nk = kernel_nodes(gr);
+    const int         nk = graph_kernel_nodes(gr);
     const cudaError_t ie = cudaGraphInstantiate(ex, gr, 0);
     cudaGraphDestroy(gr);
     if (ie != cudaSuccess) {

@@ -95,4 +95,27 @@ inline bool json_bool(const char * j, const char * key, bool fb) {
     return v ? strncmp(v, "true", 4) == 0 : fb;
 }
 
+// kernel nodes of a captured graph (the library's own launches; copies and memsets not counted)
+inline int graph_kernel_nodes(cudaGraph_t g) {
+    size_t n = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || n == 0) {
+        return 0;
+    }
+    cudaGraphNode_t * nodes = (cudaGraphNode_t *) malloc(n * sizeof(cudaGraphNode_t));
+    if (!nodes) {
+        return 0;
+    }
+    int k = 0;
+    if (cudaGraphGetNodes(g, nodes, &n) == cudaSuccess) {
+        for (size_t i = 0; i < n; i++) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) {
+                k++;
+            }
+        }
+    }
+    free(nodes);
+    return k;
+}
+
 }  // namespace acb

@@ -62,6 +62,8 @@ struct acb_qwen3_enc {
     DevBuf                         ids, pos, rope, h, xn, xq, qkv, qkv32, planes, vtb, q, k, att, gu, out, err, ws;
     int                            s_ld = 0;  // V^T row length: the sequence length rounded up to 8
     std::map<int, cudaGraphExec_t> graphs;  // one per S * 2 + exact
+    std::map<int, int>             graph_kernels;  // their kernel nodes
+    int                            last_kernels = 0;  // kernel launches of the last forward
 
     ~acb_qwen3_enc() {
         cudaSetDevice(device);
@@ -76,6 +78,7 @@ struct acb_qwen3_enc {
             cudaGraphExecDestroy(kv.second);
         }
         graphs.clear();
+        graph_kernels.clear();
     }
 
     int nqkv() const { return (c.n_heads + 2 * c.n_kv_heads) * c.head_dim; }
@@ -297,6 +300,7 @@ acb_status acb_qwen3_enc::run(int S, cudaStream_t s) {
             set_last_error("encoder graph capture failed");
             return es != ACB_OK ? es : ACB_ERR_CUDA;
         }
+        graph_kernels[key]   = graph_kernel_nodes(g);
         cudaGraphExec_t   ex = nullptr;
         const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
@@ -306,6 +310,7 @@ acb_status acb_qwen3_enc::run(int S, cudaStream_t s) {
         }
         it = graphs.emplace(key, ex).first;
     }
+    last_kernels = graph_kernels[key];
     return cudaGraphLaunch(it->second, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
 }
 
@@ -532,6 +537,10 @@ extern "C" acb_status acb_qwen3_forward_device(acb_qwen3_enc * m, const int32_t 
     ACB_TRY(m->run(S, s));
     const size_t ob = (size_t) S * m->c.hidden_size * 4;
     return cudaMemcpyAsync(d_out, m->out.p, ob, cudaMemcpyDeviceToDevice, s) == cudaSuccess ? ACB_OK : ACB_ERR_CUDA;
+}
+
+extern "C" int acb_qwen3_forward_kernels(const acb_qwen3_enc * m) {
+    return m ? m->last_kernels : 0;
 }
 
 extern "C" acb_status acb_qwen3_forward_hidden(acb_qwen3_enc * m, const float * d_hidden, int S, int layer_begin,

@@ -80,6 +80,9 @@ ACB_API acb_status acb_qwen3_forward(acb_qwen3_enc * m, const int32_t * token_id
  * range-checked on the host here; acb_qwen3_forward is the checked entry point. */
 ACB_API acb_status acb_qwen3_forward_device(acb_qwen3_enc * m, const int32_t * d_ids, int S, float * d_out,
                                             acb_stream_t stream);
+/* Kernel launches of the last forward of this stack (the nodes of its captured graph); 0 before the
+ * first. No reference counterpart: an accounting query. */
+ACB_API int        acb_qwen3_forward_kernels(const acb_qwen3_enc * m);
 
 /* qwen3_build_layers (qwen3-enc.h:249-262) over layers [layer_begin, layer_end) from caller
  * hidden states (device, [S][hidden_size] f32; the condition encoders' entry, cond-enc.h:171,
