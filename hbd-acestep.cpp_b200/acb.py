@@ -105,6 +105,10 @@ def lib():
             "acb_dit_load": (I, [C.c_char_p, I, C.POINTER(C.c_void_p)]),
             "acb_dit_weight_bytes": (C.c_size_t, [P]),
             "acb_dit_set_exact": (I, [P, I]),
+            "acb_dit_sinusoid": (I, [P, I, I, P, P]),
+            "acb_dit_sde_philox": (I, [P, P, P, P, I, I64, P]),
+            "acb_philox_randn": (I, [I64, P, I64, I, P]),
+            "acb_philox_bits": (I, [I64, I64, I64, P, P]),
             "acb_dit_forward": (I, [P, P, P, I, I, I, F, F, P, I, P]),
             "acb_dit_generate": (I, [P, P, P, P, I, I, I, I, P, P, F, P]),
             "acb_dit_generate_solver": (I, [P, P, P, P, I, I, I, I, P, P, F, I, P]),
@@ -1109,7 +1113,8 @@ class DiT:
                     enc_switch=None, real_enc_S_switch=None, dcw_scaler=0.0, stork_substeps=10, dcw_high_scaler=0.0,
                     dcw_mode="low"):
         """acb_dit_generate_ex (dit_ggml_generate's argument list). randn(seed, n) -> n floats is
-        the SDE noise source; cancel(step_count) -> bool is polled before every step. Returns
+        the SDE noise source on the host (None: the reference's Philox stream, drawn on the
+        device); cancel(step_count) -> bool is polled before every step. Returns
         (x0, device ms); raises AcbError with status 9 when cancelled."""
         np = self.np
         f32 = lambda a: None if a is None else np.ascontiguousarray(a, dtype=np.float32)
@@ -1265,6 +1270,34 @@ def dit_sde(xt, vt, noise, tt3, stream=None):
     """SDE ancestral step in place: x0 = xt - vt * tt3[0], then xt = tt3[2] * noise + (1 - tt3[2]) * x0."""
     _check("acb_dit_sde", lib().acb_dit_sde(_ptr(xt), _ptr(vt), _ptr(noise), _ptr(tt3), xt.numel(), _stream(stream)))
     return xt
+
+
+def dit_sde_philox(xt, vt, step_seeds, tt3, stream=None):
+    """SDE ancestral step in place with the noise of track b drawn on the device from the bf16
+    Philox stream of step_seeds[b] (device int64 [n_tracks]); xt, vt are [n_tracks, ...]."""
+    _check("acb_dit_sde_philox", lib().acb_dit_sde_philox(_ptr(xt), _ptr(vt), _ptr(step_seeds), _ptr(tt3),
+                                                          step_seeds.numel(), xt.numel() // step_seeds.numel(),
+                                                          _stream(stream)))
+    return xt
+
+
+def philox_randn(seed, n, bf16_round=True, out=None, device="cuda", stream=None):
+    """The reference's philox_randn(seed, out, n, bf16_round) (src/philox.h) on the device: a
+    float32 tensor [n]."""
+    import torch
+    if out is None:
+        out = torch.empty(int(n), dtype=torch.float32, device=device)
+    _check("acb_philox_randn", lib().acb_philox_randn(int(seed), _ptr(out), int(n), 1 if bf16_round else 0,
+                                                      _stream(stream)))
+    return out
+
+
+def philox_bits(seed, first, n, device="cuda", stream=None):
+    """Raw Philox4x32-10 words of counters {0, 0, first + i}, i < n, under key = seed: uint32 as int32 [n, 4]."""
+    import torch
+    out = torch.empty((int(n), 4), dtype=torch.int32, device=device)
+    _check("acb_philox_bits", lib().acb_philox_bits(int(seed), int(first), int(n), _ptr(out), _stream(stream)))
+    return out
 
 
 def attn_vt(v, Nkv, lo=False, vt_ld=None, out=None, stream=None):

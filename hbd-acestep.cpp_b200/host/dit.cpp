@@ -86,7 +86,8 @@ struct acb_dit {
     // generate
     DevBuf                          xt, vt, out, ra;
     DevBuf                          hist1, hist2;  // DPM++ 3M velocity history (previous, the one before)
-    DevBuf                          noise;         // SDE: the step's fresh noise [N][T][out_ch]
+    DevBuf                          noise;         // SDE with a host noise source: the step's fresh noise [N][T][out_ch]
+    DevBuf                          step_seeds;    // SDE on the device generator: seed_b + step + 1 per track
     DevBuf                          vpair, xall;   // sharded: [cond, uncond] velocities; gathered x0
     std::unique_ptr<DiTRun>         job;           // the step-level job (acb_dit_job_*)
     acb_stork4_tables               stork_tab{};   // the caller's ROCK4 tables (acb_dit_set_stork4_tables)
@@ -931,6 +932,7 @@ struct DiTRun {
     std::vector<float> nul;
     std::vector<int>   re_now, re_first;
     std::vector<float> tv, fresh;
+    std::vector<int64_t> seedv;  // SDE on the device generator: this step's seeds
     bool        switched = false, began = false;
     cudaStream_t s = nullptr;
     cudaEvent_t  e0 = nullptr, e1 = nullptr, done[2] = { nullptr, nullptr };
@@ -1007,7 +1009,7 @@ acb_status DiTRun::begin(acb_dit * model, acb_comm * c, const GenArgs & args, in
     if (!m || !g.noise || !g.context || !g.enc || g.N <= 0 || g.T <= 0 || g.enc_S <= 0 || n <= 0 ||
         g.T % m->c.patch_size != 0 ||
         (g.solver != ACB_SOLVER_EULER && g.solver != ACB_SOLVER_DPM3M && g.solver != ACB_SOLVER_SDE && !stk) ||
-        (sde && (!g.seeds || !g.randn)) || (half >= 0 && (n != 1 || !comm))) {
+        (sde && !g.seeds) || (half >= 0 && (n != 1 || !comm))) {
         return ACB_ERR_INVALID_ARG;
     }
     if (stk && m->stork_ms.empty()) {
@@ -1034,13 +1036,15 @@ acb_status DiTRun::begin(acb_dit * model, acb_comm * c, const GenArgs & args, in
     const size_t pair = half >= 0 ? 2 * n_per : 0;  // [cond, uncond] velocities of the track
     bool bad = m->xt.bytes < n_tot * 4 || m->vt.bytes < n_tot * 4 || m->out.bytes < n_tot * 4 ||
                m->ra.bytes < n_tot * 8 || (dpm && (m->hist1.bytes < n_tot * 4 || m->hist2.bytes < n_tot * 4)) ||
-               (sde && m->noise.bytes < n_tot * 4) || m->vpair.bytes < pair * 4;
+               (sde && g.randn && m->noise.bytes < n_tot * 4) || (sde && m->step_seeds.bytes < (size_t) n * 8) ||
+               m->vpair.bytes < pair * 4;
     if (bad) {
         m->drop_graphs();  // the graphs hold these addresses
         if (m->xt.alloc(n_tot * 4) != ACB_OK || m->vt.alloc(n_tot * 4) != ACB_OK || m->out.alloc(n_tot * 4) != ACB_OK ||
             m->ra.alloc(n_tot * 8) != ACB_OK ||
             (dpm && (m->hist1.alloc(n_tot * 4) != ACB_OK || m->hist2.alloc(n_tot * 4) != ACB_OK)) ||
-            (sde && m->noise.alloc(n_tot * 4) != ACB_OK) || (pair && m->vpair.alloc(pair * 4) != ACB_OK)) {
+            (sde && g.randn && m->noise.alloc(n_tot * 4) != ACB_OK) ||
+            (sde && m->step_seeds.alloc((size_t) n * 8) != ACB_OK) || (pair && m->vpair.alloc(pair * 4) != ACB_OK)) {
             set_last_error("DiT generate buffers allocation failed");
             return ACB_ERR_OOM;
         }
@@ -1071,7 +1075,8 @@ acb_status DiTRun::begin(acb_dit * model, acb_comm * c, const GenArgs & args, in
         stork = nullptr;
         ACB_TRY(acb_stork4_create(&m->stork_tab, (int64_t) n_tot, g.stork_substeps, &stork));
     }
-    fresh.assign(sde ? n_tot : 0, 0.0f);
+    fresh.assign(sde && g.randn ? n_tot : 0, 0.0f);
+    seedv.assign(sde ? n : 0, 0);
     tv.assign(3, 0.0f);
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
@@ -1088,7 +1093,8 @@ acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphE
     const bool dpm = g.solver == ACB_SOLVER_DPM3M, sde = g.solver == ACB_SOLVER_SDE;
     uint32_t   gbits = 0;  // the guidance scale is baked into the captured APG launch
     memcpy(&gbits, &g.guidance, 4);
-    const int  stepk = (((g.solver * 3 + hist) * 4 + first * 2 + last) * 4 + part) * 3 + (half + 1);
+    const int  sde_dev = sde && !g.randn ? 1 : 0;  // SDE noise drawn inside the graph
+    const int  stepk = ((((g.solver * 3 + hist) * 4 + first * 2 + last) * 4 + part) * 3 + (half + 1)) * 2 + sde_dev;
     const auto key   = std::make_tuple(Ng * 100000 + T, enc_S, do_cfg ? 1 : 0, stepk, m->exact ? 1 : 0, gbits);
     auto       it    = m->graphs.find(key);
     if (it != m->graphs.end()) {
@@ -1123,6 +1129,9 @@ acb_status DiTRun::get_graph(int first, int last, int hist, int part, cudaGraphE
         } else if (st == ACB_OK && dpm && !last) {
             st = acb_dit_dpm3m(m->xt.as<float>(), vv, m->hist1.as<float>(), m->hist2.as<float>(), hist,
                                m->tt.as<float>(), (int64_t) n_tot, (acb_stream_t) s);
+        } else if (st == ACB_OK && sde && !last && sde_dev) {
+            st = acb_dit_sde_philox(m->xt.as<float>(), vv, m->step_seeds.as<int64_t>(), m->tt.as<float>(), n,
+                                    (int64_t) n_per, (acb_stream_t) s);
         } else if (st == ACB_OK && sde && !last) {
             st = acb_dit_sde(m->xt.as<float>(), vv, m->noise.as<float>(), m->tt.as<float>(), (int64_t) n_tot,
                              (acb_stream_t) s);
@@ -1183,12 +1192,22 @@ acb_status DiTRun::step(int k, float t_curr, float t_next, bool last, float * ho
         }
     }
     const int first = k == 0 ? 1 : 0, lst = last ? 1 : 0, hist = dpm ? (k < 2 ? k : 2) : 0;
-    // SDE: the fresh noise of every track from its seed (solver-sde.h:28-31: seed_b + step + 1)
-    if (sde && !last) {
+    // SDE: the fresh noise of every track from its seed (solver-sde.h:28-31: seed_b + step + 1),
+    // from the caller's noise source on the host, else drawn on the device inside the step
+    if (sde && !last && g.randn) {
         for (int b = 0; b < n; b++) {
             g.randn(g.seeds[track0 + b] + k + 1, fresh.data() + (size_t) b * n_per, (int) n_per, g.randn_data);
         }
         if (cudaMemcpyAsync(m->noise.p, fresh.data(), n_tot * 4, cudaMemcpyHostToDevice, s) != cudaSuccess) {
+            return ACB_ERR_CUDA;
+        }
+    } else if (sde && !last) {
+        for (int b = 0; b < n; b++) {
+            seedv[b] = g.seeds[track0 + b] + k + 1;
+        }
+        // pageable source: staged by the call, like the timesteps below
+        if (cudaMemcpyAsync(m->step_seeds.p, seedv.data(), (size_t) n * 8, cudaMemcpyHostToDevice, s) !=
+            cudaSuccess) {
             return ACB_ERR_CUDA;
         }
     }
@@ -1358,7 +1377,7 @@ extern "C" acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, 
                                               const float * schedule, float * output, float guidance_scale,
                                               int solver, float * gpu_ms) {
     if (solver != ACB_SOLVER_EULER && solver != ACB_SOLVER_DPM3M) {
-        return ACB_ERR_INVALID_ARG;  // the SDE solver needs seeds and a noise source: acb_dit_generate_ex
+        return ACB_ERR_INVALID_ARG;  // the SDE solver needs per-track seeds: acb_dit_generate_ex
     }
     GenArgs g;
     g.noise     = noise;

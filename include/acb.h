@@ -429,6 +429,26 @@ ACB_API acb_status acb_dit_dpm3m(float * xt, const float * vt, float * prev_vt, 
  * with that seed). The last step of a schedule is acb_dit_euler with last != 0. */
 ACB_API acb_status acb_dit_sde(float * xt, const float * vt, const float * noise, const float * tt, int64_t n,
                                acb_stream_t stream);
+/* acb_dit_sde with the noise drawn inline: for track b (of n_tracks, n_per elements each) the
+ * noise is the bf16 Philox stream seeded with step_seeds[b] (device [n_tracks], the caller's
+ * seed_b + step + 1, solver-sde.h:28-31) -- the values acb_philox_randn(step_seeds[b], .., 1)
+ * writes. tt = {t_curr, t_r, t_next} on the device, as for acb_dit_sde. */
+ACB_API acb_status acb_dit_sde_philox(float * xt, const float * vt, const int64_t * step_seeds, const float * tt,
+                                      int n_tracks, int64_t n_per, acb_stream_t stream);
+
+/* ---- seeded noise (src/philox.h) ------------------------------------------------------------- */
+
+/* philox_randn (src/philox.h:130-136) on the device: out[k] (k < n, device f32) = the first
+ * Box-Muller normal of Philox4x32-10 of counter {0, 0, k} under key = seed, rounded through bf16
+ * when bf16_round (the reference always rounds: the values torch.randn gives in bf16 on a CUDA
+ * generator seeded with `seed`). Replaces the host fills of the initial noise
+ * (pipeline-synth-ops.cpp:761-770) and the SDE noise (solver-sde.h:28-31). The integer rounds are
+ * exact; the float tail uses CUDA's logf/sinf, so about one value in 10^4 differs from the
+ * reference's host stream by one bf16 step. */
+ACB_API acb_status acb_philox_randn(int64_t seed, float * out, int64_t n, int bf16_round, acb_stream_t stream);
+/* The raw Philox4x32-10 words of counters {0, 0, first + i} (i < n) under key = seed: out
+ * [n][4] u32 on the device, 16-byte aligned (philox.h:50-82, 95-107). */
+ACB_API acb_status acb_philox_bits(int64_t seed, int64_t first, int64_t n, uint32_t * out, acb_stream_t stream);
 
 /* ---- FSQ and sequence packing (the condition encoder and the FSQ (de)tokenizer) ------------- */
 

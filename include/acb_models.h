@@ -336,9 +336,10 @@ ACB_API acb_status acb_dit_generate_solver(acb_dit * m, const float * noise, con
                                            const float * enc_hidden, int enc_S, int T, int N, int num_steps,
                                            const float * schedule, float * output, float guidance_scale, int solver,
                                            float * gpu_ms);
-/* Noise source of the SDE solver: n N(0,1) samples of the stream seeded with `seed` into out. The
- * reference's is philox_randn(seed, out, n, true) (src/philox.h: Philox4x32-10, rounded to bf16);
- * a caller binding ace-synth passes that function, so trajectories match the reference's. */
+/* Host noise source of the SDE solver: n N(0,1) samples of the stream seeded with `seed` into out.
+ * The reference's is philox_randn(seed, out, n, true) (src/philox.h: Philox4x32-10, rounded to
+ * bf16). With no source (NULL) the library draws that same stream on the device inside the step
+ * (acb_dit_sde_philox), with no host fill and no copy. */
 typedef void (*acb_randn_fn)(int64_t seed, float * out, int n, void * data);
 /* dit_ggml_generate (src/dit-sampler.h:132-711) argument for argument, host arrays as in the
  * reference:
@@ -351,7 +352,8 @@ typedef void (*acb_randn_fn)(int64_t seed, float * out, int n, void * data);
  *   cancel(cancel_data): polled before every step; nonzero stops with ACB_ERR_CANCELLED (at most
  *   two steps are queued on the GPU, so it takes effect within two steps);
  *   real_S[N] / real_enc_S[N]: padding masks (:244-304; NULL: no padding);
- *   seeds[N] + randn / randn_data: the SDE solver's per-step noise (seed_b + step + 1);
+ *   seeds[N] + randn / randn_data: the SDE solver's per-step noise (seed_b + step + 1): randn
+ *   NULL draws it on the device (the reference's philox_randn stream), else on the host;
  *   use_batch_cfg: accepted, both values run the batched graph (results equal up to summation order);
  *   dcw_scaler / dcw_high_scaler / dcw_mode: DCW after every ODE step but the last (either scaler
  *   > 0; modes "low" (also NULL or unknown), "high", "double", "pix"; acb_dit_dcw), not with SDE;

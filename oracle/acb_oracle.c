@@ -983,6 +983,52 @@ void orc_timestep_embedding(float t, int dim, int max_period, float * out) {
     }
 }
 
+/* ---- Philox noise (src/philox.h) ---- */
+
+/* One round: two 32x32->64 products of the even words, the odd words and the key XORed into the
+ * high halves (philox.h:37-47). Round multipliers and Weyl key increments (philox.h:16-19) are the
+ * published Philox4x32 constants. */
+void orc_philox4x32_10(const uint32_t ctr[4], uint32_t k0, uint32_t k1, uint32_t out[4]) {
+    uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3];
+    for (int r = 0; r < 10; r++) {
+        if (r) {
+            k0 += 0x9E3779B9u;
+            k1 += 0xBB67AE85u;
+        }
+        const uint64_t p0 = (uint64_t) 0xD2511F53u * c0;
+        const uint64_t p1 = (uint64_t) 0xCD9E8D57u * c2;
+        const uint32_t n0 = (uint32_t) (p1 >> 32) ^ c1 ^ k0;
+        const uint32_t n2 = (uint32_t) (p0 >> 32) ^ c3 ^ k1;
+        c0 = n0;
+        c1 = (uint32_t) p1;
+        c2 = n2;
+        c3 = (uint32_t) p0;
+    }
+    out[0] = c0;
+    out[1] = c1;
+    out[2] = c2;
+    out[3] = c3;
+}
+
+/* Only the first output of the first Box-Muller pair is kept (philox.h:85-91, 130-136): a uniform
+ * u in (0, 1] from word 0 and an angle in (0, 2 pi) from word 1, both as x * 2^-32 + half a step
+ * in float; normal = sqrt(-2 ln u) * sin(angle). */
+void orc_philox_randn(int64_t seed, int64_t n, int bf16_round, float * out) {
+    const float inv32 = 2.3283064365386963e-10f;   /* 2^-32 */
+    const float inv32_2pi = 1.4629180792671596e-09f; /* 2 pi 2^-32 */
+    const uint32_t k0 = (uint32_t) (uint64_t) seed, k1 = (uint32_t) ((uint64_t) seed >> 32);
+#pragma omp parallel for schedule(static) if (n > 65536)
+    for (int64_t k = 0; k < n; k++) {
+        const uint32_t ctr[4] = { 0u, 0u, (uint32_t) (uint64_t) k, (uint32_t) ((uint64_t) k >> 32) };
+        uint32_t       w[4];
+        orc_philox4x32_10(ctr, k0, k1, w);
+        const float u = (float) w[0] * inv32 + inv32 * 0.5f;
+        const float v = (float) w[1] * inv32_2pi + inv32_2pi * 0.5f;
+        const float z = sqrtf(-2.0f * logf(u)) * sinf(v);
+        out[k] = bf16_round ? orc_bf16_to_f32(orc_f32_to_bf16(z)) : z;
+    }
+}
+
 /* ---- FSQ (src/fsq-detok.h:14-29, src/fsq-tok.h:42-60) ---- */
 
 static const int orc_fsq_levels[6] = { 8, 8, 8, 5, 5, 5 };

@@ -124,6 +124,13 @@ void orc_attention(const float * q, int64_t q_tok_stride, const void * k, const 
 /* Sinusoidal timestep embedding (ggml_timestep_embedding, dim even): out[dim]. */
 void orc_timestep_embedding(float t, int dim, int max_period, float * out);
 
+/* Philox4x32-10 (Salmon et al., "Parallel random numbers: as easy as 1, 2, 3", SC'11) of one
+ * 128-bit counter under a 64-bit key, as src/philox.h:30-82 computes it. */
+void orc_philox4x32_10(const uint32_t ctr[4], uint32_t k0, uint32_t k1, uint32_t out[4]);
+/* philox_randn (src/philox.h:130-136): out[k] = the first Box-Muller normal of counter
+ * {0, 0, k_lo, k_hi} under key = seed, rounded through bfloat16 when bf16_round. */
+void orc_philox_randn(int64_t seed, int64_t n, int bf16_round, float * out);
+
 /* FSQ alphabet {8,8,8,5,5,5}: fsq_decode_index (src/fsq-detok.h:18-29) and fsq_encode_index
  * (src/fsq-tok.h:42-60, libm tanhf). */
 void orc_fsq_decode_index(int index, float * out6);

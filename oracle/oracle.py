@@ -55,6 +55,8 @@ def lib():
             "orc_mul_mat": (I, [I, P, I64, I64, P, I64, P]),
             "orc_attention": (None, [P, I64, P, P, I, I64, I64, P, P, I64, I64, I64, I, I, I, F]),
             "orc_timestep_embedding": (None, [F, I, I, P]),
+            "orc_philox4x32_10": (None, [P, C.c_uint32, C.c_uint32, P]),
+            "orc_philox_randn": (None, [I64, I64, I, P]),
             "orc_set_threads": (None, [I]),
             "orc_set_mul_mat_mode": (None, [I]),
             "orc_get_mul_mat_mode": (I, []),
@@ -266,6 +268,21 @@ def attention(q, k, v, kv_type, mask, scale, kv_head_major=False):
 def timestep_embedding(t, dim=256, max_period=10000):
     out = np.empty(dim, dtype=np.float32)
     lib().orc_timestep_embedding(t, dim, max_period, _p(out))
+    return out
+
+
+def philox4x32_10(ctr, key):
+    """Philox4x32-10 of one counter (4 x u32) under key (2 x u32): 4 x u32 (src/philox.h:50-82)."""
+    c = np.ascontiguousarray(ctr, dtype=np.uint32)
+    out = np.empty(4, dtype=np.uint32)
+    lib().orc_philox4x32_10(_p(c), int(key[0]) & 0xFFFFFFFF, int(key[1]) & 0xFFFFFFFF, _p(out))
+    return out
+
+
+def philox_randn(seed, n, bf16_round=True):
+    """philox_randn (src/philox.h:130-136): the reference's seeded N(0, 1) noise, float32 [n]."""
+    out = np.empty(n, dtype=np.float32)
+    lib().orc_philox_randn(int(seed), int(n), 1 if bf16_round else 0, _p(out))
     return out
 
 

@@ -9,6 +9,10 @@ Fixtures:
                     Q8_0 / Q4_K / Q6_K blocks (the blocks themselves are stored too, so the check
                     needs no quantizer). gguf-py's Q8_0 path is documented as bit-exact with
                     ggml-quants.c (gguf/quants.py:378-394).
+  philox_golden.npz the reference's own Philox noise (src/philox.h, through tests/test-philox.cpp
+                    compiled into oracle/_ref/ by `make -C oracle ref REFERENCE=...`): for each
+                    seed its first 8192 bf16 values as uint16 bits, and the SHA-256 of the full
+                    192000-value dump (64 channels x 25 Hz x 120 s, the reference test's size).
   lm_golden.npz     a tiny seeded Qwen3 causal LM (F32 weights stored as float16-representable
                     values) and the first-token-position logits of a prompt computed by the
                     reference's own fp32 PyTorch restatement test_pytorch_logits
@@ -105,16 +109,47 @@ def make_lm(rng, reference: str) -> dict:
     return out
 
 
+PHILOX_SEEDS = [42, 0, 1, -1, 123456789, 2**32 + 5, 2**40 + 7, 9223372036854775807, -9223372036854775808]
+PHILOX_FULL = 64 * 25 * 120
+
+
+def make_philox(reference: str) -> dict:
+    import hashlib
+    import subprocess
+    oracle_dir = os.path.join(HERE, "..", "..", "oracle")
+    subprocess.run(["make", "-s", "-C", oracle_dir, "ref", f"REFERENCE={os.path.abspath(reference)}"], check=True)
+    exe = os.path.join(oracle_dir, "_ref", "test-philox")
+    bits, digests = [], []
+    with tempfile.TemporaryDirectory() as td:
+        dump = os.path.join(td, "noise.f32")
+        for seed in PHILOX_SEEDS:
+            subprocess.run([exe, str(seed), str(PHILOX_FULL), dump], check=True, capture_output=True)
+            v = np.fromfile(dump, dtype=np.float32)
+            assert v.size == PHILOX_FULL and not (v.view(np.uint32) & 0xFFFF).any()  # bf16-representable
+            bits.append((v[:8192].view(np.uint32) >> 16).astype(np.uint16))
+            digests.append(hashlib.sha256(v.tobytes()).hexdigest())
+    return {"seeds": np.array(PHILOX_SEEDS, dtype=np.int64), "bf16_bits": np.stack(bits),
+            "full_n": np.int64(PHILOX_FULL), "full_sha256": np.array(digests)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ACB_REFERENCE"),
                     help="checkout of the reference project (or set ACB_REFERENCE)")
+    ap.add_argument("--only", choices=["quant", "lm", "philox"], action="append",
+                    help="write only these fixtures (default: all)")
     a = ap.parse_args()
     if not a.reference:
         ap.error("give the reference checkout with --reference or ACB_REFERENCE")
+    only = set(a.only or ["quant", "lm", "philox"])
     rng = np.random.default_rng(20261201)
-    np.savez_compressed(os.path.join(HERE, "quant_golden.npz"), **make_quant(rng))
-    np.savez_compressed(os.path.join(HERE, "lm_golden.npz"), **make_lm(rng, a.reference))
+    quant = make_quant(rng)  # drawn first in every run, so the LM fixture sees the same rng state
+    if "quant" in only:
+        np.savez_compressed(os.path.join(HERE, "quant_golden.npz"), **quant)
+    if "lm" in only:
+        np.savez_compressed(os.path.join(HERE, "lm_golden.npz"), **make_lm(rng, a.reference))
+    if "philox" in only:
+        np.savez_compressed(os.path.join(HERE, "philox_golden.npz"), **make_philox(a.reference))
     print("wrote", sorted(os.listdir(HERE)))
 
 

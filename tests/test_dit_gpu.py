@@ -239,6 +239,29 @@ def test_dit_generate_dcw_matches_oracle(cuda, tmp_path):
     dit.close()
 
 
+@pytest.mark.parametrize("t,t_r", [(1.0, 1.0), (0.75, 0.25), (0.3, 0.0), (0.0, 0.0)])
+def test_dit_sinusoid_matches_oracle(cuda, t, t_r):
+    """acb_dit_sinusoid (dit_ggml_build_temb, dit-graph.h:81-117): row 0 embeds t * 1000, row 1
+    (t - t_r) * 1000, cos half then sin half. The device's expf/cosf/sinf and the host libm's may
+    differ by a few ulp; with arguments up to 1000 that moves a channel by at most ~4e-4, so the
+    bar is 1e-3 absolute. At t = 1 both rows also match the reference's CPU-backend dump
+    (tests/CPU-Q8_0.log:162-163) to that bar."""
+    import torch
+    tt = torch.tensor([t, t_r], dtype=torch.float32, device=cuda)
+    out = torch.empty((2, 256), dtype=torch.float32, device=cuda)
+    acb._check("acb_dit_sinusoid", acb.lib().acb_dit_sinusoid(tt.data_ptr(), 256, 10000, out.data_ptr(),
+                                                               acb._stream(None)))
+    got = out.cpu().numpy()
+    a = np.float32(t) * np.float32(1000.0)
+    b = np.float32(np.float32(t) - np.float32(t_r)) * np.float32(1000.0)
+    assert np.abs(got[0] - O.timestep_embedding(a)).max() <= 1e-3
+    assert np.abs(got[1] - O.timestep_embedding(b)).max() <= 1e-3
+    if t == 1.0 and t_r == 1.0:
+        assert np.abs(got[0, :4] - [0.562379, 0.789627, 0.439928, -0.023645]).max() <= 1e-3
+        assert np.array_equal(got[1], np.concatenate([np.ones(128), np.zeros(128)]).astype(np.float32))
+    assert acb.lib().acb_dit_sinusoid(None, 256, 10000, out.data_ptr(), acb._stream(None)) == 1
+
+
 def test_dit_config4_width_matches_oracle(cuda, tmp_path):
     """Config 4 layer shapes (hidden 2048, FFN 6144, 16/8 heads, 1500 frames -> 750 tokens with
     the 128 sliding window, 512 condition rows) with 2 layers and 2 sequences."""
@@ -290,6 +313,32 @@ def test_dpm3m_solver_steps_match_oracle(cuda):
             assert np.array_equal(prev2.cpu().numpy(), pp_ref)
     with pytest.raises(acb.AcbError):  # a negative history is rejected before any launch
         acb.dit_dpm3m(xt, vd, prev, prev2, -1, tt)
+
+
+def test_dit_generate_sde_device_noise_matches_oracle(cuda, tmp_path):
+    """The SDE solver with no host noise source: the library draws the reference's Philox stream
+    (seed_b + step + 1, bf16) inside each step; the oracle's generate gets the oracle's Philox
+    (pinned to the reference's own dump) as its source. Same bars as every generate."""
+    cfg = DIT_TINY
+    path, keep = _model(tmp_path, cfg, seed=16)
+    dit = acb.DiT(path)
+    od = O.dit_from_gguf_tensors(cfg, keep)
+    null = keep["null_condition_emb"][1].astype(np.float32)
+    rng = np.random.default_rng(17)
+    N, T, enc_S, Oc = 2, 64, 16, cfg["out_channels"]
+    noise = np.stack([O.philox_randn(s, T * Oc).reshape(T, Oc) for s in (77, 78)])
+    ctx = rng.standard_normal((N, T, cfg["in_channels"] - Oc)).astype(np.float32)
+    enc = rng.standard_normal((N, enc_S, cfg["enc_hidden_size"])).astype(np.float32)
+    sched = acb.turbo_schedule(4)
+    seeds = [77, 2**35 + 3]
+    x0, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver="sde", seeds=seeds)
+    ref = O.dit_generate(od, noise, ctx, enc, null, sched, 3.0, solver="sde", seeds=seeds, randn=O.philox_randn)
+    _check(x0, ref, 0.9999, 1e-2, "sde device noise")
+    # the host source given the same stream lands on the same trajectory
+    x1, _ = dit.generate_ex(noise, ctx, enc, sched, guidance_scale=3.0, solver="sde", seeds=seeds,
+                            randn=O.philox_randn)
+    _check(x1, x0, 0.9999, 1e-2, "sde host vs device noise")
+    dit.close()
 
 
 def test_sde_solver_steps_match_oracle(cuda):
