@@ -513,6 +513,11 @@ def run_ours(args):
             print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="f16 operands, f32 accumulation")),
                   flush=True)
         return
+    if args.workloads == "noise":
+        r = run_noise(dev, rank, want_cpu=not args.no_cpu_baseline)
+        if rank == 0:
+            print(json.dumps(dict(r, n_gpus=ws, data="synthetic", dtype="u32 rounds, f32 Box-Muller")), flush=True)
+        return
     if args.workloads == "enc":
         r = run_enc(dev, rank, want_cpu=not args.no_cpu_baseline)
         if rank == 0:
@@ -560,6 +565,9 @@ def run_ours(args):
             if "condlog" in wl:
                 torch.cuda.empty_cache()
                 line["cond_logged_case"] = run_cond_logged(dev, rank)
+            if "noise" in wl:
+                torch.cuda.empty_cache()
+                line["philox_noise"] = run_noise(dev, rank, want_cpu=not args.no_cpu_baseline)
         if "lm5" in wl:
             # config 5's LM shards one sequence per GPU: run at every N (all ranks take part)
             torch.cuda.empty_cache()
@@ -1313,6 +1321,91 @@ def run_vae(dev, rank, want_cpu=True, T=VAE_T, reps=10):
     return res
 
 
+NOISE_N = 1 << 26  # 64 Mi values, 256 MiB of output: twice the L2
+
+
+def run_noise(dev, rank, want_cpu=True, reps=20):
+    """The reference's seeded noise (src/philox.h philox_randn: Philox4x32-10 + Box-Muller, bf16):
+    device fill of 64 Mi values, and end to end the host fill that the pipeline makes per
+    generate (pipeline-synth-ops.cpp:761-770: 4 tracks x 2170 frames x 64 channels) through
+    acb_philox_randn + a copy into pinned host memory. CPU arm: the reference's own
+    tests/test-philox binary (oracle/_ref, compiled from its sources) when present, else the
+    oracle port (bit-identical to it)."""
+    import subprocess
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import acb
+
+    out = torch.empty(NOISE_N, dtype=torch.float32, device=dev)
+    for i in range(3):
+        acb.philox_randn(i, NOISE_N, out=out)
+    torch.cuda.synchronize()
+    ms_all = []
+    for i in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        acb.philox_randn(100 + i, NOISE_N, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_all.append(e0.elapsed_time(e1))
+    ms = float(np.median(ms_all))
+    vps = NOISE_N / (ms * 1e-3)
+    n_e2e = 4 * 2170 * 64
+    host = torch.empty(n_e2e, dtype=torch.float32).pin_memory()
+    buf = torch.empty(n_e2e, dtype=torch.float32, device=dev)
+    for i in range(3):
+        acb.philox_randn(i, n_e2e, out=buf)
+        host.copy_(buf, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_reps = 50
+    t0 = time.perf_counter()
+    for i in range(e2e_reps):
+        acb.philox_randn(1000 + i, n_e2e, out=buf)
+        host.copy_(buf, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - t0) / e2e_reps
+    peaks, kind = measured_peaks()
+    gbs = NOISE_N * 4 / (ms * 1e-3) / 1e9
+    res = {
+        "metric": "seeded noise values per second (philox_randn: Philox4x32-10 + Box-Muller, bf16-rounded)",
+        "value": round(vps / 1e9, 2), "unit": "Gvalues/s", "higher_is_better": True, "ms_per_fill": round(ms, 4),
+        "config": {"workload": "philox_randn_64Mi", "values": NOISE_N, "l2": "output 256 MiB > L2"},
+        "roofline": {"kernel": "philox_randn_kernel", "bound": "alu (10 multiply-high rounds + log/sin/sqrt per "
+                     "value; 4 bytes written)", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                     "peak_kind": kind, "unit": "GB/s written", "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "bytes_per_fill": NOISE_N * 4, "traffic": None},
+        "e2e": {"value": round(n_e2e / e2e_s / 1e9, 3), "unit": "Gvalues/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": n_e2e * 4, "ms_per_call": round(e2e_s * 1e3, 3),
+                "path": "acb_philox_randn + copy to pinned host: one generate's initial noise, 4 x 2170 x 64"},
+        "gpu_launches_per_fill": 1,
+    }
+    if want_cpu:
+        n = 1 << 22
+        exe = os.path.join(ROOT, "oracle", "_ref", "test-philox")
+        if os.access(exe, os.X_OK):
+            with tempfile.TemporaryDirectory() as td:
+                t0 = time.perf_counter()
+                subprocess.run([exe, "42", str(n), os.path.join(td, "n.f32")], check=True, capture_output=True)
+                dt = time.perf_counter() - t0
+            cpu = {"kind": "reference", "sample": f"the reference's tests/test-philox, {n} values, one thread "
+                                                  "(process start and a 16 MiB file write included)"}
+        else:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle as O
+            before = O.get_threads()
+            O.set_threads(1)
+            t0 = time.perf_counter()
+            O.philox_randn(42, n)
+            dt = time.perf_counter() - t0
+            O.set_threads(before)
+            cpu = {"kind": "port", "sample": f"oracle philox_randn, {n} values, one thread"}
+        res["cpu_baseline"] = dict(cpu, value=round(n / dt / 1e9, 4), unit="Gvalues/s", cores=1)
+    return res
+
+
 DIT_TRACKS, DIT_T, DIT_ENC_S, DIT_STEPS, DIT_GUIDANCE = 4, 1500, 512, 8, 3.0
 
 
@@ -1857,7 +1950,7 @@ def main():
     ap.add_argument("--lm-prompt", type=int, default=LM_PROMPT)
     ap.add_argument("--lm-gen", type=int, default=LM_GEN)
     ap.add_argument("--lm5-gen", type=int, default=LM5_GEN, help="config 5 LM tokens (profiling runs use fewer)")
-    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,ditlog,condlog,lm5,dit5",
+    ap.add_argument("--workloads", default="dit,ops,lm,enc,vae,ditlog,condlog,noise,lm5,dit5",
                     help="comma list: dit (config 4, the headline line, every N), ops (config 2), lm (config 3 "
                          "decode), enc (config 1 text encoder), vae (the audio decoder on 86.8 s), ditlog (the DiT "
                          "generation the reference logs: 1 track, turbo, no CFG), condlog (the conditioning it logs) -- "
