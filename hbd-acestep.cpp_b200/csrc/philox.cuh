@@ -7,7 +7,7 @@
 // a thread needs no state. The integer rounds are exact; the Box-Muller arithmetic is written with
 // explicitly rounded operations (nvcc must not fuse its multiply-adds, the reference's CPU code does
 // not), and the transcendental calls are CUDA's logf / sinf / sqrt, which agree with the host libm
-// to a few ulp -- after the bfloat16 rounding the streams differ in about one element in 10^4,
+// to a few ulp -- after the bfloat16 rounding the streams differ in at most 1 element in 1000,
 // by one bfloat16 step.
 #pragma once
 

@@ -443,7 +443,7 @@ ACB_API acb_status acb_dit_sde_philox(float * xt, const float * vt, const int64_
  * when bf16_round (the reference always rounds: the values torch.randn gives in bf16 on a CUDA
  * generator seeded with `seed`). Replaces the host fills of the initial noise
  * (pipeline-synth-ops.cpp:761-770) and the SDE noise (solver-sde.h:28-31). The integer rounds are
- * exact; the float tail uses CUDA's logf/sinf, so about one value in 10^4 differs from the
+ * exact; the float tail uses CUDA's logf/sinf, so at most 1 in 1000 values differs from the
  * reference's host stream by one bf16 step. */
 ACB_API acb_status acb_philox_randn(int64_t seed, float * out, int64_t n, int bf16_round, acb_stream_t stream);
 /* The raw Philox4x32-10 words of counters {0, 0, first + i} (i < n) under key = seed: out
